@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Benchmark of the tallymap B200 backend on BASELINE config 2: the 1-D random walk, N = 4,194,304 items per GPU.
+
+One STEP = the forward launch plus the reverse-mode gradient launch (w.r.t. the broadcast `drift`) over the step's
+items: "Mitems/s fwd & grad".  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
+second) are synthetic, made with jax.random's algorithm on the host (tallymap_b200.prng).  Weak scaling: each rank
+runs its own 4,194,304 items (a contiguous slice of the global item set) and the partial tallies are combined with
+one NCCL collective step (all_reduce of the f32 / i32 tallies, all_gather + on-device combine of the exact gradient
+words).
+
+  python bench.py [--gpus N --steps K --warmup W]            # this backend (N > 1: under torchrun)
+  python bench.py --impl reference [...]                    # the reference's CPU path, timed on the host cores
+
+Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events on the launching stream, L2 flushed
+(a 256 MiB write) between steps outside the events; barrier + synchronize around the timed loop; the max over ranks.
+`e2e` repeats the step through the public API (tallymap_b200.vmap(...).value_and_grad) from pinned host inputs,
+copies and the result read-back inside the timed region.  `roofline`: the walkers are integer-issue bound (two
+threefry2x32 per step, 79 INT32 ops each, dominate); the peak is the same device's measured threefry2x32 rate at
+full occupancy (tm_probe_threefry), so frac = the fraction of issue-rate speed of light the kernel reaches.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ITEMS = 4194304
+MAX_STEPS = 20000
+C_CKPT = 16
+TF_OPS = 79          # INT32 ops per threefry2x32 (2 XOR + 2 ADD + 20 x (ADD, ROTL, XOR) + 5 x 3 ADD)
+METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
+CONFIG = {"workload": "1-D random walk (BASELINE config 2): forward + grad w.r.t. drift", "items_per_gpu": N_ITEMS,
+          "max_steps": MAX_STEPS, "tally": "Sum((256,)) f32 + Sum((2,)) f32, per-item k int32",
+          "rev_checkpoints": C_CKPT, "l2": "flushed between timed steps (256 MiB write)"}
+
+
+def rw_inputs(n, start=0):
+    from tallymap_b200 import prng
+    kx, ks = prng.split(prng.PRNGKey(1), 2)
+    return prng.uniform(kx, n, start=start), prng.split(ks, n, start=start)
+
+
+def replay_micro_steps(K, C=C_CKPT):
+    """loop-step evaluations of the checkpointed replay (count, checkpoint, advance + fill, sweep) for trip counts K,
+    summed: the schedule of tallymap/_reverse.py:343-440."""
+    ks, cnt = np.unique(np.asarray(K, np.int64), return_counts=True)
+    m = np.maximum(C, (ks + C - 1) // C)
+    ns = (ks + m - 1) // m
+    tot = ks + np.where(ns > 1, (ns - 1) * m, 0)           # count pass + checkpoint pass
+    for s in range(C):
+        L = np.clip(ks - s * m, 0, m)
+        live = (s < ns) & (L > 0)
+        nsub = (L + C - 1) // C
+        for u in range(int(nsub.max()) if live.any() else 0):
+            LL = np.clip(L - u * C, 0, C)
+            ok = live & (u < nsub)
+            first = (s == 0) & (u == 0)
+            fill = np.where(first, 0, u * C + LL - 1)
+            tot = tot + np.where(ok, fill + LL, 0)
+    return int((tot * cnt).sum())
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region (SM clock, throttle reasons)."""
+    Q = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus = bus_id          # the PCI bus number of this rank's device (torch), or None
+        self.rows, self.proc, self.err = [], None, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError as e:
+            self.err = str(e)
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.rows.append([c.strip() for c in ln.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        def bus(r):
+            try:
+                return int(r[1].split(":")[1], 16)
+            except (IndexError, ValueError):
+                return None
+        rows = [r for r in self.rows if len(r) >= 10]
+        mine = [r for r in rows if self.bus is not None and bus(r) == self.bus] or rows
+        if not mine:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": self.err or "nvidia-smi unavailable"}
+        sm = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in mine for n, v in zip(names, r[6:10]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(mine[0][3]) if mine[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(mine)}
+
+
+# ------------------------------------------------------------------------------------------------ reference arm
+def cpu_sample(n_target_s, nthreads, x, k, log=None):
+    """oracle port (the reference CPU kernel target's model, f32 tallies) on a prefix of the items, sized to about
+    n_target_s seconds of fwd + grad: -> (items, seconds, Mitems/s)"""
+    from oracle import oracle
+    n = 4096
+    while True:
+        t0 = time.perf_counter()
+        oracle.rw_fwd(x[:n], k[:n], 1.0, nthreads=nthreads, f64acc=False)
+        oracle.rw_grad(x[:n], k[:n], 1.0, np.ones(256, np.float32), nthreads=nthreads)
+        dt = time.perf_counter() - t0
+        if dt >= n_target_s or n >= len(x):
+            return n, dt, n / dt / 1e6
+        n = min(len(x), max(n * 2, int(n * n_target_s / max(dt, 1e-3) * 0.9)))
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle
+    oracle.build()
+    nth = len(os.sched_getaffinity(0))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    x, k = rw_inputs(N_ITEMS)
+    n, dt, _ = cpu_sample(2.0, nth, x, k)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.rw_fwd(x[:n], k[:n], 1.0, nthreads=nth, f64acc=False)
+        oracle.rw_grad(x[:n], k[:n], 1.0, np.ones(256, np.float32), nthreads=nth)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    v = n / (ms / 1e3) / 1e6
+    sample = f"first {n} of the {N_ITEMS} items per step (fwd + grad), f32 tallies, {nth} OpenMP threads"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "Mitems/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm, host)",
+        "config": dict(CONFIG, sample_items=n),
+        "cpu_baseline": {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "Mitems/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (JAX) cannot run on this image (jax is not installed, no network): this is the "
+                "oracle/ C++ restatement of its CPU kernel target"}), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--items", type=int, default=N_ITEMS, help="items per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if args.warmup < 3:
+        raise SystemExit("bench.py: at least 3 warm-up steps")
+
+    import torch
+    import torch.distributed as dist
+
+    import tallymap_b200 as tm
+    from tallymap_b200 import _lib
+    from tallymap_b200 import backend as B
+    from tallymap_b200 import parallel
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    N = args.items
+    start = rank * N
+    x_h, k_h = rw_inputs(N, start)
+    x0 = torch.from_numpy(x_h).to(dev)
+    keys = torch.from_numpy(k_h.view(np.int32)).to(dev)
+    drift = torch.tensor(1.0, device=dev)
+    ct_hist = torch.ones(256, device=dev)
+    ct_side = torch.zeros(2, device=dev)
+    fo = B.alloc_results(B.RW_FWD, N, dev)
+    go = B.alloc_results(B.RW_GRAD, N, dev)
+    g_all = torch.zeros(1, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    glayout, _ = B.RW_GRAD.result_layout(N)
+    gnames = [n for n, _, _, _ in glayout]
+
+    def fwd():
+        out = B.run(B.RW_FWD, [x0, keys], [drift], consts=(MAX_STEPS,), out=fo)
+        if world > 1:
+            parallel.all_reduce_sums(out[:3])
+        return out
+
+    def grad():
+        out = B.run(B.RW_GRAD, [x0, keys], [drift, ct_hist, ct_side], consts=(MAX_STEPS,), out=go)
+        if world > 1:
+            parallel.combine_exact(go[gnames.index("ct_drift.exact")], 1, g_all, go[gnames.index("stats")])
+        return out
+
+    for _ in range(args.warmup):
+        fwd()
+        grad()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(getattr(torch.cuda.get_device_properties(dev), "pci_bus_id", None))
+    clocks.start()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        fwd()
+        ev[i][1].record(stream)
+        grad()
+        ev[i][2].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    f_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
+    g_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    t = torch.tensor([f_ms + g_ms, f_ms, g_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tot_ms, f_ms, g_ms = (float(v) / args.steps for v in t.tolist())
+    value = N * world / (tot_ms / 1e3) / 1e6
+
+    # ---- e2e: the public API from pinned host inputs, H2D + both launches + result read-back timed
+    f = tm.vmap("walk1d", outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None),
+                max_steps=MAX_STEPS)
+    xp = torch.from_numpy(x_h).pin_memory()
+    kp = torch.from_numpy(k_h.view(np.int32)).pin_memory()
+    cts = {"hist": ct_hist}
+    d2h = [0]
+
+    def e2e_step():
+        r, g = f.value_and_grad(xp, kp, drift, wrt=2, cotangents=cts)
+        outs = [r.outputs["hist"], r.outputs["side"], r.stats["n_truncated"].reshape(1), g.reshape(1)]
+        if world > 1:
+            parallel.all_reduce_sums(outs[:3])
+        host = [o.to("cpu") for o in outs]
+        d2h[0] = sum(h.numel() * h.element_size() for h in host)
+        return host
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_ms = 0.0
+    for i in range(args.steps):
+        flush.zero_()
+        e0.record(stream)
+        e2e_step()
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms += e0.elapsed_time(e1)
+    te = torch.tensor([e2e_ms / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = N * world / (float(te.item()) / 1e3) / 1e6
+
+    # ---- roofline of the dominant kernel: threefry2x32 evaluations per second against the probe's
+    kk = fo[-2].to("cpu").numpy()
+    steps_total = int(kk.astype(np.int64).sum())
+    tf_fwd = 2 * steps_total
+    tf_grad = 2 * replay_micro_steps(kk)
+    import ctypes
+    pout = torch.empty(148 * 2048 * 2, dtype=torch.int32, device=dev)
+    used = ctypes.c_int64()
+    pe = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    iters = 4096
+    for rep in range(3):
+        pe[0].record(stream)
+        _lib.check(_lib.lib().tm_probe_threefry(ctypes.c_void_p(stream.cuda_stream), iters,
+                                                ctypes.c_void_p(pout.data_ptr()), pout.numel(), ctypes.byref(used)))
+        pe[1].record(stream)
+    torch.cuda.synchronize()
+    peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
+    dom = ("rw_grad", tf_grad, g_ms) if g_ms >= f_ms else ("rw_fwd", tf_fwd, f_ms)
+    achieved = dom[1] / (dom[2] / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nth = len(os.sched_getaffinity(0))
+        n, dt, v = cpu_sample(10.0, nth, x_h, k_h)
+        cpu = {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port",
+               "sample": f"oracle port (reference CPU kernel target model, f32 tallies): fwd + grad of the first {n} "
+                         f"items, {dt:.1f} s on {nth} OpenMP threads"}
+    info = _lib.kernel_info(_lib.kernel_id("rw_grad")[0])
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm on the host, seed 1)",
+        "config": dict(CONFIG, items_total=N * world, parallelism=f"items sharded over {world} GPU(s)"),
+        "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3),
+        "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),
+        "grad_mitems_s": round(N * world / (g_ms / 1e3) / 1e6, 3),
+        "mean_trip_count": round(steps_total / N, 2),
+        "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
+                "h2d_bytes_per_step": int(x_h.nbytes + k_h.nbytes), "d2h_bytes_per_step": int(d2h[0])},
+        "gpu_launches": args.steps * (2 + (1 if world > 1 else 0)),
+        "roofline": {"bound": "issue", "kernel": dom[0], "achieved": round(achieved, 2), "peak": round(peak, 2),
+                     "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
+                     "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
+                     "work": f"{dom[1]} threefry2x32 per launch (2 per loop step; steps from the per-item trip counts)"},
+        "clocks": clk,
+        "kernel_resources": info,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

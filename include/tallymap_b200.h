@@ -1,0 +1,102 @@
+/* tallymap_b200: the C ABI of the B200 kernel backend for tallymap.
+ *
+ * This is the drop-in boundary below tallymap's kernel-backend driver.  In the reference the driver
+ * (tallymap/backends/kernel/__init__.py:135-185, KB.run) reaches the device through ONE XLA FFI custom call,
+ * "tallymap_cuda_launch", handled by tallymap/backends/kernel/shim.cc; the entry points below are what that shim
+ * exports and what its handler does, as plain C: pointers, sizes and a stream, no XLA, JAX or torch types.
+ *
+ * Buffers: every launch takes ONE array of device pointers, the program's inputs first (per-item operands,
+ * broadcast operands, hoisted constants), then its results (sum tallies, scratch accumulators, the control words,
+ * stats int32[5], per-item results) -- the order of the reference's SjParams (backends/kernel/kernel.py:570-596).
+ * The first n_zero results are zeroed on the stream before the kernel runs (shim.cc:210-219).
+ *
+ * Errors: every entry point returns 0 on success and a nonzero TM_E* code otherwise; tm_last_error() returns the
+ * calling thread's last message.  Launches are asynchronous on the caller's stream; nothing here synchronises.
+ */
+#ifndef TALLYMAP_B200_H
+#define TALLYMAP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TM_OK = 0,
+  TM_EINVAL = 1,   /* bad id, buffer count, size or pointer (the FFI handler's kInvalidArgument) */
+  TM_ECUDA = 2,    /* a CUDA runtime call failed (kInternal); the message names it */
+  TM_EDEVICE = 3   /* tm_check_status: the device error word of a finished launch is set */
+};
+
+/* ABI version of this header (bumped on any signature or buffer-layout change). */
+int tm_abi_version(void);
+
+/* The calling thread's last error message ("" when none). */
+const char* tm_last_error(void);
+
+/* Look up a built-in (ahead-of-time compiled, sm_100a) kernel by program name, e.g. "rw_fwd", "rw_grad".
+ * *id receives its kernel id; *n_buffers the number of buffer pointers a launch takes (may be NULL).
+ * Replaces: the kernel cache lookup of backends/kernel/__init__.py:106-128 (kernel(), keyed by a digest). */
+int tm_kernel_id(const char* name, int64_t* id, int32_t* n_buffers);
+
+/* Enumerate the built-in kernels: *name receives the i-th name (NULL past the end). */
+int tm_kernel_name(int32_t i, const char** name);
+
+/* Register a kernel image (a cubin or fatbin for sm_100a containing `extern "C" __global__ tm_main(Params, int64)`,
+ * from the runtime lowering) under `id`; re-registering an id keeps the first image.  The image is copied and loaded
+ * lazily on each device at its first launch.  n_buffers: the pointers a launch takes; smem_bytes: its dynamic shared
+ * memory; block: threads per block.
+ * Replaces: tallymap_register (backends/kernel/shim.cc:134-142). */
+int tm_register(int64_t id, const void* image, size_t n, const char* note, int32_t n_buffers, int32_t smem_bytes,
+                int32_t block);
+
+/* Resources of a kernel on the current device: out[7] = registers per thread, local bytes per thread, static
+ * shared bytes per block, resident blocks per SM, SMs, max resident threads per SM, block size.
+ * Replaces: tallymap_kernel_info (backends/kernel/shim.cc:147-155). */
+int tm_kernel_info(int64_t id, long long* out);
+
+/* Launch kernel `id` on `stream` (a cudaStream_t; NULL = the legacy default stream) over n_items items.
+ *   bufs[n_args + n_rets]: device pointers, inputs then results; ret_bytes[n_rets]: each result's size in bytes
+ *   n_zero: the first n_zero results are zeroed (cudaMemsetAsync on `stream`) before the launch
+ *   flags: bit 2 (4): the grid is not capped by n_items (a program that spawns children)
+ *   status: optional (may be NULL); receives the cudaError_t of the launch (0: launched)
+ * The grid is one persistent block per resident slot (SMs x blocks per SM at the kernel's occupancy), capped at
+ * ceil(n_items / block).
+ * Replaces: the body of the XLA FFI handler SjLaunchImpl (backends/kernel/shim.cc:157-239). */
+int tm_launch(int64_t id, void* stream, void* const* bufs, int32_t n_args, int32_t n_rets, const size_t* ret_bytes,
+              int32_t n_zero, int32_t flags, int64_t n_items, int32_t* status);
+
+/* The cross-GPU step of an exact f32 tally (TSpec.exact): `words` holds n_src exact scratch buffers end to end
+ * (each: n_bins x 5 int64 carry-save words, then one uint32 flag per bin packed into (n_bins + 1) / 2 uint64), e.g.
+ * every rank's buffer after an all-gather; out[n_bins] receives the correctly rounded f32 of the exact total (NaN
+ * for a flagged or overflowing bin, counted in stats[3]).
+ * Replaces: the psum of a kernel-backend call's tallies under sharding (tallymap/_primitive.py:245-262), for the
+ * exact cotangent tallies whose words cannot be summed word by word without carries. */
+int tm_exact_combine(void* stream, const void* words, int32_t n_src, int32_t n_bins, float* out, int32_t* stats);
+
+/* Exact f32 scatter-add: out[b] = the correctly rounded sum of every vals[i] with bins[i] == b (out-of-range bins
+ * dropped and counted in stats[4]; non-finite values make their bin NaN, counted in stats[3]).  `words` is caller
+ * scratch of (n_bins x 5 + (n_bins + 1) / 2) uint64, zeroed here.
+ * Replaces: the exact accumulator of a Sum(fixed_point=True) float32 output (backends/kernel/kernel.py:870-941,
+ * DENSE), on its own. */
+int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins, void* words,
+                     float* out, int32_t* stats);
+
+/* Calibration probe for rooflines: `iters` threefry2x32 evaluations per thread on every resident thread slot of
+ * the device (at most out_len threads, a multiple of 128), no memory traffic besides one word per thread.
+ * *threads_used receives the thread count.  Time it on `stream` for the device's threefry issue rate.
+ * (No counterpart in the reference, which reports no rooflines.) */
+int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used);
+
+/* Read a finished launch's device error word (ctl[3] of its control-word buffer, host-visible copy `ctl_host`,
+ * 8 uint32 words).  Returns TM_OK when it is clear, TM_EDEVICE (with a message) when a device-side wait gave up or
+ * a bounds check failed. */
+int tm_check_status(const uint32_t* ctl_host);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TALLYMAP_B200_H */

@@ -1,0 +1,175 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes front end of the CPU oracle (a C++/OpenMP restatement of the reference's CPU
+kernel target for the benchmark item programs; see oracle_core.h, oracle_run.h, programs.cpp).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm may import this module, and only as
+the checker or the timed CPU baseline: the product (tallymap_b200) never calls it.
+
+The library is built with -march=native, so it is built per host CPU (the GPU box's host differs from the build
+container's): one .so per CPU model under oracle/_build/.
+"""
+import ctypes
+import hashlib
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LOCK = threading.Lock()
+_LIB = None
+
+
+def _cpu_tag():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith(("model name", "flags")):
+                    model += ln
+    except OSError:
+        pass
+    return hashlib.sha256(model.encode()).hexdigest()[:12]
+
+
+def lib_path():
+    return os.path.join(HERE, "_build", f"liboracle-{_cpu_tag()}.so")
+
+
+def build(force=False):
+    """compile the oracle for this host's CPU (make; a few seconds) -> path of the .so."""
+    path = lib_path()
+    srcs = [os.path.join(HERE, f) for f in os.listdir(HERE) if f.endswith((".cpp", ".h"))]
+    if not force and os.path.exists(path) and all(os.path.getmtime(s) <= os.path.getmtime(path) for s in srcs):
+        return path
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    os.replace(os.path.join(HERE, "_build", "liboracle.so"), path)
+    return path
+
+
+def lib():
+    global _LIB
+    with _LOCK:
+        if _LIB is None:
+            L = ctypes.CDLL(build())
+            P = ctypes.c_void_p
+            i64, i32, f32, u32 = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_uint32
+            L.or_num_threads.restype = ctypes.c_int
+            L.or_threefry2x32.argtypes = [u32, u32, u32, u32, P]
+            L.or_split.argtypes = [u32, u32, i64, P]
+            L.or_uniform.argtypes = [u32, u32, i64, f32, f32, P]
+            L.or_exact_sum.argtypes = [P, P, i64, ctypes.c_int, P, P]
+            L.or_exact_words.argtypes = [P, P, i64, ctypes.c_int, P]
+            L.or_exact_read.argtypes = [P, P]
+            L.or_exact_read.restype = f32
+            L.or_q1_fwd.argtypes = [i64, P, P, f32, i32, ctypes.c_int, P, P, P, P, ctypes.c_int]
+            L.or_q1_grad.argtypes = [i64, P, P, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
+            L.or_rw_fwd.argtypes = [i64, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
+            L.or_rw_grad.argtypes = [i64, P, P, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
+            _LIB = L
+    return _LIB
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def num_threads():
+    return lib().or_num_threads()
+
+
+# ----------------------------------------------------------------------------------------------- RNG / exact sum
+def threefry2x32(k0, k1, c0, c1):
+    out = np.zeros(2, np.uint32)
+    lib().or_threefry2x32(int(k0), int(k1), int(c0), int(c1), _p(out))
+    return int(out[0]), int(out[1])
+
+
+def split(key, n):
+    out = np.zeros((n, 2), np.uint32)
+    lib().or_split(int(key[0]), int(key[1]), n, _p(out))
+    return out
+
+
+def uniform(key, n, lo=0.0, hi=1.0):
+    out = np.zeros(n, np.float32)
+    lib().or_uniform(int(key[0]), int(key[1]), n, lo, hi, _p(out))
+    return out
+
+
+def exact_sum(vals, bins, nb):
+    vals = np.ascontiguousarray(vals, np.float32)
+    bins = np.ascontiguousarray(bins, np.int32)
+    out = np.zeros(nb, np.float32)
+    stats = np.zeros(5, np.int32)
+    lib().or_exact_sum(_p(vals), _p(bins), len(vals), nb, _p(out), _p(stats))
+    return out, stats
+
+
+def exact_words(vals, bins, nb):
+    vals = np.ascontiguousarray(vals, np.float32)
+    bins = np.ascontiguousarray(bins, np.int32)
+    w = np.zeros((nb, 5), np.int64)
+    lib().or_exact_words(_p(vals), _p(bins), len(vals), nb, _p(w))
+    return w
+
+
+def exact_read(words):
+    w = np.ascontiguousarray(words, np.int64)
+    bad = np.zeros(1, np.int32)
+    o = lib().or_exact_read(_p(w), _p(bad))
+    return np.float32(o), bool(bad[0])
+
+
+# ----------------------------------------------------------------------------------------------- programs
+def q1_fwd(x0, keys, theta, max_steps=100, nthreads=1, f64acc=True):
+    """f64acc: f32 tallies accumulated in f64 and rounded once (the checker); False: the reference host target's f32
+    partials (the timed CPU baseline)."""
+    x0 = np.ascontiguousarray(x0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    n = len(x0)
+    hist = np.zeros(16, np.float32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_q1_fwd(n, _p(x0), _p(keys), float(theta), max_steps, nthreads, _p(hist), _p(k), _p(tr), _p(st),
+                    int(f64acc))
+    return dict(hist=hist, k=k, trunc=tr.astype(bool), stats=st)
+
+
+def q1_grad(x0, keys, theta, ct, max_steps=100, C=16, nthreads=1):
+    x0 = np.ascontiguousarray(x0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    ct = np.ascontiguousarray(ct, np.float32)
+    n = len(x0)
+    g = np.zeros(1, np.float32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_q1_grad(n, _p(x0), _p(keys), float(theta), _p(ct), max_steps, C, nthreads, _p(g), _p(tr), _p(st))
+    return dict(g=g, trunc=tr.astype(bool), stats=st)
+
+
+def rw_fwd(x0, keys, drift, max_steps=20000, nthreads=1, f64acc=True):
+    x0 = np.ascontiguousarray(x0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    n = len(x0)
+    hist = np.zeros(256, np.float32)
+    side = np.zeros(2, np.float32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_rw_fwd(n, _p(x0), _p(keys), float(drift), max_steps, nthreads, _p(hist), _p(side), _p(k), _p(tr),
+                    _p(st), int(f64acc))
+    return dict(hist=hist, side=side, k=k, trunc=tr.astype(bool), stats=st)
+
+
+def rw_grad(x0, keys, drift, ct, max_steps=20000, C=16, nthreads=1):
+    x0 = np.ascontiguousarray(x0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    ct = np.ascontiguousarray(ct, np.float32)
+    n = len(x0)
+    g = np.zeros(1, np.float32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_rw_grad(n, _p(x0), _p(keys), float(drift), _p(ct), max_steps, C, nthreads, _p(g), _p(tr), _p(st))
+    return dict(g=g, trunc=tr.astype(bool), stats=st)

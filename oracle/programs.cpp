@@ -1,0 +1,309 @@
+// TEST INFRASTRUCTURE ONLY -- CPU restatements of the benchmark item programs, forward and reverse, in the
+// reference's CPU kernel-target execution model (oracle_run.h) and arithmetic (oracle_core.h): single-rounding f32
+// arithmetic with no FMA (compiled -ffp-contract=off, backends/kernel/host.py:35), emits as _emit_rule
+// (backends/kernel/kernel.py:984-1003: an index outside [0, S) is dropped and counted in stats[4]), the max_steps
+// cap as retrace(cap) (tallymap/_rewrite.py:517-528: loop while k < M && pred; truncated iff k >= M && pred(out)),
+// and reverse mode as vjp_prog (_reverse.py:1079-1180): the checkpointed loop, VJPs of one step newest first, the
+// broadcast operand's cotangent accumulated in f32 across the sweep (ctb + db, _reverse.py:387) and emitted once per
+// item into an exact tally (_reverse.py:1172-1176).
+//
+// The item functions are the benchmark configurations written as tallymap items (jax-style pseudo code in each
+// struct's comment).  Exposed through a plain C ABI for ctypes (oracle/oracle.py).
+#include <cstdio>
+#include <vector>
+
+#include "oracle_run.h"
+
+using namespace orc;
+
+namespace {
+
+// The flush of a privatised sum tally.  The reference's host target keeps f32 partials and adds them with an IEEE
+// compare-and-swap loop (Acc = float: the timed CPU baseline).  The checker mode (Acc = double) keeps partials and
+// the shared output in f64 and rounds once at the end, so a parity tolerance measures the kernel's own summation
+// error, not the checker's.
+template <class Acc>
+static inline void add_out(Acc* o, Acc v) {
+  std::atomic_ref<Acc>(*o).fetch_add(v, std::memory_order_relaxed);
+}
+
+// ================================================================================================= Q1: quickstart
+// examples/quickstart.py:19-30 with max_steps=100:
+//   def walker(t, x, key, theta):
+//     def body(c):
+//       k, x, t = c
+//       u = uniform(fold_in(key, k))
+//       t = t.add("hist", (x * 16).astype(int32), theta * (1.0 - x))
+//       return k + 1, x * (0.5 + 0.5 * u), t
+//     k, x, t = while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
+//     return t, k
+struct Q1State { i32 kc, k; float x; };
+
+struct Q1Base {
+  const float* x0;
+  const u32* keys;
+  float theta;
+  i32 M;
+  Key key(i64 i) const { return Key{keys[2 * i], keys[2 * i + 1]}; }
+  bool pred(float x) const { return x > 0.05f; }
+};
+
+template <class Acc>
+struct Q1Fwd : Q1Base {
+  Acc* hist;           // [16]
+  i32* k_out;          // [N]
+  uint8_t* trunc;      // [N]
+  i32* stats;          // [5]
+  struct Priv { Acc h[16] = {}; };
+  void item(i64 i, Priv& p) const {
+    const Key kk = key(i);
+    float x = x0[i];
+    i32 k = 0, kc = 0;
+    while (kc < M && pred(x)) {
+      ++kc;
+      const float u = uniform_f32(fold_in(kk, (u32)k), 0u, 0.0f, 1.0f);
+      const i32 b = f2i_rz(x * 16.0f);
+      const float v = theta * (1.0f - x);
+      if ((u32)b >= 16u) stat_add(stats, 4, 1); else p.h[b] += v;
+      k = k + 1;
+      x = x * (0.5f + 0.5f * u);
+    }
+    trunc[i] = (kc >= M && pred(x)) ? 1 : 0;
+    k_out[i] = k;
+  }
+  void flush(Priv& p) const {
+    for (int b = 0; b < 16; ++b) if (p.h[b] != 0) add_out(&hist[b], p.h[b]);
+  }
+};
+
+// grad of <ct_hist, hist> w.r.t. theta.  The step VJP: the emit's transpose gathers ct at the emitted index (0 when
+// out of range, _tally.py:72-82); mul's transpose gives ct_val * (1 - x); x does not depend on theta (not active).
+struct Q1Grad : Q1Base {
+  const float* ct;     // [16] cotangent of hist
+  int C;
+  float* g_theta;      // [1] readout
+  uint8_t* trunc;      // [N]: the replay's own truncation flags
+  i32* stats;
+  ExactBins* gbins;
+  struct Adj { float ctb; };
+  struct Priv { ExactBins b{1}; };
+  bool cond(const Q1State& s) const { return s.kc < M && pred(s.x); }
+  Key kk;              // (per-item: set in item(); a copy of the struct per item)
+  Q1State step(const Q1State& s) const {
+    const float u = uniform_f32(fold_in(kk, (u32)s.k), 0u, 0.0f, 1.0f);
+    return Q1State{s.kc + 1, s.k + 1, s.x * (0.5f + 0.5f * u)};
+  }
+  void vjp_step(const Q1State& s, Adj& a) const {
+    const i32 b = f2i_rz(s.x * 16.0f);
+    const float cv = ((u32)b < 16u) ? ct[b] : 0.0f;
+    const float db = cv * (1.0f - s.x);
+    a.ctb = a.ctb + db;
+  }
+  void item(i64 i, Priv& p) const {
+    Q1Grad me = *this;
+    me.kk = key(i);
+    Adj a{0.0f};
+    Q1State fin;
+    checkpointed_while(me, Q1State{0, 0, x0[i]}, C, a, &fin, [](const Q1State&, Adj&) {});
+    trunc[i] = (fin.kc >= M && pred(fin.x)) ? 1 : 0;
+    exact_emit_priv(p.b, 0, a.ctb, stats);
+  }
+  void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
+};
+
+// ================================================================================================= RW: 1-D walk
+//   def walk(t, x, key, drift):
+//     def body(c):
+//       k, x, t = c
+//       u = uniform(fold_in(key, k))
+//       t = t.add("hist", (x * 256).astype(int32), drift * x)
+//       return k + 1, x + 0.02 * (2 * u - 1), t
+//     k, x, t = while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+//     t = t.add("side", (x > 1).astype(int32), 1.0)
+//     return t, k
+// max_steps = 20,000.
+struct RWState { i32 kc, k; float x; };
+
+struct RWBase {
+  const float* x0;
+  const u32* keys;
+  float drift;
+  i32 M;
+  Key key(i64 i) const { return Key{keys[2 * i], keys[2 * i + 1]}; }
+  static bool pred(float x) { return x >= 0.0f && x <= 1.0f; }
+  static float move(float x, float u) { return x + 0.02f * (2.0f * u - 1.0f); }
+};
+
+template <class Acc>
+struct RWFwd : RWBase {
+  Acc* hist;           // [256]
+  Acc* side;           // [2]
+  i32* k_out;
+  uint8_t* trunc;
+  i32* stats;
+  struct Priv { Acc h[256] = {}; Acc s[2] = {}; };
+  void item(i64 i, Priv& p) const {
+    const Key kk = key(i);
+    float x = x0[i];
+    i32 k = 0, kc = 0;
+    while (kc < M && pred(x)) {
+      ++kc;
+      const float u = uniform_f32(fold_in(kk, (u32)k), 0u, 0.0f, 1.0f);
+      const i32 b = f2i_rz(x * 256.0f);
+      const float v = drift * x;
+      if ((u32)b >= 256u) stat_add(stats, 4, 1); else p.h[b] += v;
+      k = k + 1;
+      x = move(x, u);
+    }
+    p.s[x > 1.0f ? 1 : 0] += (Acc)1.0f;
+    trunc[i] = (kc >= M && pred(x)) ? 1 : 0;
+    k_out[i] = k;
+  }
+  void flush(Priv& p) const {
+    for (int b = 0; b < 256; ++b) if (p.h[b] != 0) add_out(&hist[b], p.h[b]);
+    for (int b = 0; b < 2; ++b) if (p.s[b] != 0) add_out(&side[b], p.s[b]);
+  }
+};
+
+// grad of <ct_hist, hist> + <ct_side, side> w.r.t. drift: side does not depend on drift; the step VJP is
+// ct_hist[bin] * x (0 for a dropped emit).
+struct RWGrad : RWBase {
+  const float* ct;     // [256]
+  int C;
+  uint8_t* trunc;
+  i32* stats;
+  ExactBins* gbins;
+  Key kk;
+  struct Adj { float ctb; };
+  struct Priv { ExactBins b{1}; };
+  bool cond(const RWState& s) const { return s.kc < M && pred(s.x); }
+  RWState step(const RWState& s) const {
+    const float u = uniform_f32(fold_in(kk, (u32)s.k), 0u, 0.0f, 1.0f);
+    return RWState{s.kc + 1, s.k + 1, move(s.x, u)};
+  }
+  void vjp_step(const RWState& s, Adj& a) const {
+    const i32 b = f2i_rz(s.x * 256.0f);
+    const float cv = ((u32)b < 256u) ? ct[b] : 0.0f;
+    a.ctb = a.ctb + cv * s.x;
+  }
+  void item(i64 i, Priv& p) const {
+    RWGrad me = *this;
+    me.kk = key(i);
+    Adj a{0.0f};
+    RWState fin;
+    checkpointed_while(me, RWState{0, 0, x0[i]}, C, a, &fin, [](const RWState&, Adj&) {});
+    trunc[i] = (fin.kc >= M && pred(fin.x)) ? 1 : 0;
+    exact_emit_priv(p.b, 0, a.ctb, stats);
+  }
+  void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
+};
+
+}  // namespace
+
+// ================================================================================================= C ABI
+extern "C" {
+
+int or_num_threads(void) { return omp_get_max_threads(); }
+
+void or_threefry2x32(u32 k0, u32 k1, u32 c0, u32 c1, u32* out) { threefry2x32(k0, k1, c0, c1, &out[0], &out[1]); }
+
+// split(key, n) -> out[n][2]
+void or_split(u32 k0, u32 k1, i64 n, u32* out) {
+  for (i64 i = 0; i < n; ++i) {
+    const Key k = split_at(Key{k0, k1}, (u32)i);
+    out[2 * i] = k.a;
+    out[2 * i + 1] = k.b;
+  }
+}
+
+// uniform(key, (n,), f32, lo, hi) -> out[n]
+void or_uniform(u32 k0, u32 k1, i64 n, float lo, float hi, float* out) {
+  for (i64 i = 0; i < n; ++i) out[i] = uniform_f32(Key{k0, k1}, (u32)i, lo, hi);
+}
+
+// the exact sum of vals into bins (out-of-range bins dropped), read out as the kernel's exact tally
+void or_exact_sum(const float* vals, const i32* bins, i64 n, int nb, float* out, i32* stats) {
+  ExactBins g(nb);
+  for (i64 i = 0; i < n; ++i) {
+    if ((u32)bins[i] >= (u32)nb) continue;
+    if (exact_emit<false>(&g.w[(size_t)bins[i] * kExactWords], vals[i])) { stats[3] += 1; g.flag[bins[i]] = 1; }
+  }
+  exact_readout(g, nb, out, stats);
+}
+
+// the raw words of an exact sum (test of the word layout): words[nb][5]
+void or_exact_words(const float* vals, const i32* bins, i64 n, int nb, i64* words) {
+  ExactBins g(nb);
+  for (i64 i = 0; i < n; ++i)
+    if ((u32)bins[i] < (u32)nb) exact_emit<false>(&g.w[(size_t)bins[i] * kExactWords], vals[i]);
+  for (size_t j = 0; j < g.w.size(); ++j) words[j] = g.w[j];
+}
+
+float or_exact_read(const i64* words, int* bad) {
+  bool b = false;
+  const float o = exact_read(words, &b);
+  *bad = b ? 1 : 0;
+  return o;
+}
+
+// f64acc: 0 = the reference's f32 partials (timed baseline), 1 = f64 partials rounded once (checker)
+int or_q1_fwd(i64 n, const float* x0, const u32* keys, float theta, i32 max_steps, int nthreads, float* hist,
+              i32* k_out, uint8_t* trunc, i32* stats, int f64acc) {
+  if (f64acc) {
+    std::vector<double> h(16, 0.0);
+    Q1Fwd<double> p;
+    p.x0 = x0; p.keys = keys; p.theta = theta; p.M = max_steps;
+    p.hist = h.data(); p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+    team_run(p, n, nthreads);
+    for (int b = 0; b < 16; ++b) hist[b] = (float)h[b];
+    return 0;
+  }
+  Q1Fwd<float> p;
+  p.x0 = x0; p.keys = keys; p.theta = theta; p.M = max_steps;
+  p.hist = hist; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+  team_run(p, n, nthreads);
+  return 0;
+}
+
+int or_q1_grad(i64 n, const float* x0, const u32* keys, float theta, const float* ct, i32 max_steps, int C,
+               int nthreads, float* g_theta, uint8_t* trunc, i32* stats) {
+  ExactBins g(1);
+  Q1Grad p;
+  p.x0 = x0; p.keys = keys; p.theta = theta; p.M = max_steps; p.ct = ct; p.C = C;
+  p.trunc = trunc; p.stats = stats; p.gbins = &g;
+  team_run(p, n, nthreads);
+  exact_readout(g, 1, g_theta, stats);
+  return 0;
+}
+
+int or_rw_fwd(i64 n, const float* x0, const u32* keys, float drift, i32 max_steps, int nthreads, float* hist,
+              float* side, i32* k_out, uint8_t* trunc, i32* stats, int f64acc) {
+  if (f64acc) {
+    std::vector<double> h(256, 0.0), sd(2, 0.0);
+    RWFwd<double> p;
+    p.x0 = x0; p.keys = keys; p.drift = drift; p.M = max_steps;
+    p.hist = h.data(); p.side = sd.data(); p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+    team_run(p, n, nthreads);
+    for (int b = 0; b < 256; ++b) hist[b] = (float)h[b];
+    for (int b = 0; b < 2; ++b) side[b] = (float)sd[b];
+    return 0;
+  }
+  RWFwd<float> p;
+  p.x0 = x0; p.keys = keys; p.drift = drift; p.M = max_steps;
+  p.hist = hist; p.side = side; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+  team_run(p, n, nthreads);
+  return 0;
+}
+
+int or_rw_grad(i64 n, const float* x0, const u32* keys, float drift, const float* ct, i32 max_steps, int C,
+               int nthreads, float* g_drift, uint8_t* trunc, i32* stats) {
+  ExactBins g(1);
+  RWGrad p;
+  p.x0 = x0; p.keys = keys; p.drift = drift; p.M = max_steps; p.ct = ct; p.C = C;
+  p.trunc = trunc; p.stats = stats; p.gbins = &g;
+  team_run(p, n, nthreads);
+  exact_readout(g, 1, g_drift, stats);
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+"""The user-facing layer over the backend: `vmap(item, outputs, in_axes, max_steps)` returning `Result`, and the
+reverse-mode gradient of a mapped call with respect to a broadcast operand, with the reference's result contract
+(tallymap/_api.py:180-195, 681-698, 898-958):
+
+  * outputs: the summed tallies; EVERY float output is NaN when a resource limit intervened (an item hit
+    max_steps, counted in stats['n_truncated']); integer outputs and per-item results are never poisoned;
+  * per_item: the item's per-item results; truncated: bool[N];
+  * stats: spawned, children_dropped, children_truncated, fixed_point_overflow, dropped_emits, n_truncated.
+
+A gradient is ONE replay launch (the adjoint program recomputes every item from its inputs: _api.py:951-958) whose
+own truncation flags poison the cotangent (_primitive.py:586-594).
+
+Items are lowered programs (backend.ItemProgram families).  JAX is not a dependency: an item is named by its
+program family rather than traced from a Python function.
+"""
+import dataclasses
+from typing import Any, NamedTuple
+
+import torch
+
+from . import backend as B
+
+
+@dataclasses.dataclass(frozen=True)
+class Sum:
+    """a summed output of a fixed shape (tallymap.Sum, _api.py:55-84)."""
+    shape: tuple
+    dtype: torch.dtype = torch.float32
+
+    def __post_init__(self):
+        object.__setattr__(self, "shape", tuple(int(s) for s in self.shape))
+
+
+class Result(NamedTuple):
+    outputs: dict
+    per_item: Any
+    truncated: Any
+    stats: dict
+
+
+@dataclasses.dataclass(frozen=True)
+class Family:
+    """an item program in its forward and reverse forms.  in_axes: the item's (0 | None) per argument (the
+    per-item operands first, then broadcast ones, as the programs lay them out); grads: broadcast operand index ->
+    its adjoint program; ys: which per-item results the item returns (besides the truncation flag)."""
+    name: str
+    fwd: B.ItemProgram
+    grads: dict
+    in_axes: tuple
+    default_max_steps: int
+
+
+FAMILIES = {
+    "quickstart": Family("quickstart", B.Q1_FWD, {0: B.Q1_GRAD}, (0, 0, None), 100),
+    "walk1d": Family("walk1d", B.RW_FWD, {0: B.RW_GRAD}, (0, 0, None), 20000),
+}
+
+
+def _poison(outs, bad):
+    """NaN for every float output when `bad` (a select, so a clean call is bitwise unchanged: _api.py:916-925)."""
+    return {n: (torch.where(bad, torch.full_like(v, float("nan")), v) if v.is_floating_point() else v)
+            for n, v in outs.items()}
+
+
+class Mapped:
+    """tallymap.vmap(item, outputs, in_axes, max_steps) over a lowered item family."""
+
+    def __init__(self, fam, outputs, in_axes, max_steps):
+        self.fam = fam
+        names = [t.name for t in fam.fwd.tallies]
+        if sorted(outputs) != sorted(names):
+            raise KeyError(f"tallymap_b200: item {fam.name!r} writes outputs {names}, got {sorted(outputs)}")
+        for t in fam.fwd.tallies:
+            o = outputs[t.name]
+            if tuple(o.shape) != tuple(t.shape) or o.dtype != t.dtype:
+                raise TypeError(f"tallymap_b200: output {t.name!r} is Sum({t.shape}, {t.dtype}) in this item, got "
+                                f"Sum({o.shape}, {o.dtype})")
+        if tuple(in_axes) != tuple(fam.in_axes):
+            raise ValueError(f"tallymap_b200: item {fam.name!r} maps in_axes={fam.in_axes}, got {tuple(in_axes)}")
+        self.max_steps = int(fam.default_max_steps if max_steps is None else max_steps)
+        if self.max_steps < 1:
+            raise ValueError("tallymap_b200: max_steps must be >= 1")
+
+    def _split(self, args):
+        if len(args) != len(self.fam.in_axes):
+            raise TypeError(f"tallymap_b200: item {self.fam.name!r} takes {len(self.fam.in_axes)} arguments")
+        pi = [a for a, ax in zip(args, self.fam.in_axes) if ax == 0]
+        bc = [a for a, ax in zip(args, self.fam.in_axes) if ax is None]
+        return pi, bc
+
+    def __call__(self, *args):
+        pi, bc = self._split(args)
+        p = self.fam.fwd
+        out = B.run(p, pi, bc, consts=(self.max_steps,))
+        nt = len(p.tallies)
+        tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
+        stats_raw = out[nt]
+        ys = out[nt + 1:]
+        trunc = ys[p.trunc].bool()
+        per = [y for i, y in enumerate(ys) if i != p.trunc]
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        outs = _poison(tallies, n_tr > 0)
+        return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+
+    def value_and_grad(self, *args, wrt, cotangents):
+        """(Result, gradient) of one forward and one replay launch, with the inputs moved to the device once."""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        moved = []
+        for a, ax in zip(args, self.fam.in_axes):
+            if ax == 0:
+                t = a if isinstance(a, torch.Tensor) else torch.from_numpy(B._host(a))
+                moved.append(t.to(dev, non_blocking=True))
+            else:
+                moved.append(a)
+        return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
+
+    def grad(self, *args, wrt, cotangents):
+        """d <cotangents, outputs> / d args[wrt] for a broadcast operand `wrt` (argument index): one replay launch.
+        cotangents: {output name: array of the output's shape}; missing outputs get zero cotangents."""
+        if self.fam.in_axes[wrt] is not None:
+            raise ValueError("tallymap_b200: grad with respect to a per-item operand is not built for this item")
+        bidx = sum(1 for ax in self.fam.in_axes[:wrt] if ax is None)
+        if bidx not in self.fam.grads:
+            raise NotImplementedError(f"tallymap_b200: item {self.fam.name!r} has no adjoint for argument {wrt}")
+        pi, bc = self._split(args)
+        g = self.fam.grads[bidx]
+        cts = []
+        for t in self.fam.fwd.tallies:
+            c = cotangents.get(t.name)
+            cts.append(torch.zeros(t.shape, dtype=t.dtype) if c is None else c)
+        out = B.run(g, pi, list(bc) + cts, consts=(self.max_steps,))
+        ct = out[0].reshape(())
+        trunc = out[len(g.tallies) + 1 + g.trunc]
+        return torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
+
+
+def vmap(item, outputs, in_axes, max_steps=None):
+    fam = FAMILIES[item] if isinstance(item, str) else item
+    return Mapped(fam, outputs, in_axes, max_steps)

@@ -1,0 +1,204 @@
+"""The kernel-backend driver: `run(p, pi, bc, ...)`, the B200 counterpart of the reference's KB.run
+(tallymap/backends/kernel/__init__.py:135-185), and the item programs it can launch.
+
+An ItemProgram here describes one lowered item program and its buffer layout.  `run` marshals the operands the way
+KB.run does -- [per-item operands] [broadcast operands] [hoisted constants] -- allocates the results
+[sum tallies] [scratch accumulators] [control words] [stats int32[5]] [per-item results], lets the launcher zero the
+first n_zero of them, launches through the C ABI on the current CUDA stream, and returns, in the reference's output
+order (backends/kernel/__init__.py:177-185, _primitive._abstract): [sum tallies] + [stats] + [per-item results].
+Keys enter as uint32[..., 2] key data (__init__.py:131-132).
+
+Everything runs on the GPU through libtm_b200.so; there is no CPU path.  Device memory and streams come from torch.
+"""
+import dataclasses
+from typing import Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+
+STATS = ("spawned", "children_dropped", "children_truncated", "fixed_point_overflow", "dropped_emits")
+CTL_WORDS = 8
+EXACT_WORDS = 5
+
+
+@dataclasses.dataclass(frozen=True)
+class TSpec:
+    """a Sum tally of the program (tallymap/_api.py:204-220): flat size S, dtype; exact: the f32 sum is kept as 5
+    carry-save int64 words per bin (a scratch buffer) and read out correctly rounded."""
+    name: str
+    shape: Tuple[int, ...]
+    dtype: torch.dtype = torch.float32
+    exact: bool = False
+
+    @property
+    def S(self):
+        return int(np.prod(self.shape, dtype=np.int64)) if self.shape else 1
+
+
+@dataclasses.dataclass(frozen=True)
+class Operand:
+    name: str
+    shape: Tuple[int, ...]          # per-item operands: the shape of ONE item's value
+    dtype: torch.dtype
+
+
+@dataclasses.dataclass(frozen=True)
+class ItemProgram:
+    """one lowered program: its kernel and its operand / result layout.
+    pi: per-item operands; bc: broadcast operands (for an adjoint: then the output cotangents); consts: hoisted
+    int32 constants (max_steps); tallies: sum outputs; ys: per-item results; trunc: index of the truncation flag in
+    ys (None: no max_steps cap); grad_of: for an adjoint, the (forward program name, broadcast operand index) it
+    differentiates."""
+    name: str
+    kernel: str
+    pi: Tuple[Operand, ...]
+    bc: Tuple[Operand, ...]
+    consts: Tuple[str, ...]
+    tallies: Tuple[TSpec, ...]
+    ys: Tuple[Operand, ...]
+    trunc: int = None
+    spawns: bool = False
+
+    @property
+    def n_args(self):
+        return len(self.pi) + len(self.bc) + 1
+
+    def result_layout(self, N):
+        """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero."""
+        out = []
+        for t in self.tallies:
+            out.append((t.name, t.S * _itemsize(t.dtype), t.dtype, t.shape))
+        for t in self.tallies:
+            if t.exact:
+                # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
+                n64 = t.S * EXACT_WORDS + (t.S + 1) // 2
+                out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
+        out.append(("ctl", CTL_WORDS * 4, torch.int32, (CTL_WORDS,)))
+        out.append(("stats", len(STATS) * 4, torch.int32, (len(STATS),)))
+        n_zero = len(out)
+        for y in self.ys:
+            out.append((y.name, N * int(np.prod(y.shape, dtype=np.int64)) * _itemsize(y.dtype), y.dtype,
+                        (N,) + tuple(y.shape)))
+        return out, n_zero
+
+
+def _itemsize(dt):
+    return torch.empty((), dtype=dt).element_size()
+
+
+_U32 = torch.int32   # uint32 key data travels as int32 bits (torch has no full uint32 arithmetic; bits only)
+
+# -------------------------------------------------------------------------------------------------- programs
+# The benchmark items (BASELINE configs 1 and 2), forward and reverse.  Buffer layouts: csrc/items_walks.cuh.
+_F32 = torch.float32
+KEY = Operand("key", (2,), _U32)
+
+Q1_FWD = ItemProgram("q1_fwd", "q1_fwd", pi=(Operand("x", (), _F32), KEY), bc=(Operand("theta", (), _F32),),
+                     consts=("max_steps",), tallies=(TSpec("hist", (16,)),),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
+Q1_GRAD = ItemProgram("q1_grad", "q1_grad", pi=(Operand("x", (), _F32), KEY),
+                      bc=(Operand("theta", (), _F32), Operand("ct_hist", (16,), _F32)), consts=("max_steps",),
+                      tallies=(TSpec("ct_theta", (1,), exact=True),),
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0)
+RW_FWD = ItemProgram("rw_fwd", "rw_fwd", pi=(Operand("x", (), _F32), KEY), bc=(Operand("drift", (), _F32),),
+                     consts=("max_steps",), tallies=(TSpec("hist", (256,)), TSpec("side", (2,))),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
+RW_GRAD = ItemProgram("rw_grad", "rw_grad", pi=(Operand("x", (), _F32), KEY),
+                      bc=(Operand("drift", (), _F32), Operand("ct_hist", (256,), _F32), Operand("ct_side", (2,), _F32)),
+                      consts=("max_steps",), tallies=(TSpec("ct_drift", (1,), exact=True),),
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD)}
+
+
+# -------------------------------------------------------------------------------------------------- run
+def _host(x):
+    """a numpy operand as a contiguous array torch accepts (uint32 key data travels as int32 bits)"""
+    a = np.asarray(x)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return np.ascontiguousarray(a)
+
+
+def _dev(x, device, dtype):
+    if isinstance(x, torch.Tensor):
+        t = x
+    else:
+        t = torch.from_numpy(_host(x))
+    if t.dtype == torch.uint32:
+        t = t.view(torch.int32)
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    return t.to(device, non_blocking=True).contiguous()
+
+
+def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, **_):
+    """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
+    and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
+    as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
+    of `run.last` (for tm_check_status).  target must be 'cuda' (no CPU fallback, as the reference's kernel
+    backend never falls back: _primitive.py:189-194).  out: optional preallocated result buffers (as returned by
+    alloc_results), reused without reallocation."""
+    if target != "cuda":
+        raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
+    if not torch.cuda.is_available():
+        raise RuntimeError("tallymap_b200: no CUDA device")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if len(pi) != len(p.pi) or len(bc) != len(p.bc):
+        raise TypeError(f"{p.name}: expected {len(p.pi)} per-item and {len(p.bc)} broadcast operands, "
+                        f"got {len(pi)} and {len(bc)}")
+    args = [_dev(x, dev, o.dtype) for x, o in zip(pi, p.pi)]
+    N = int(args[0].shape[0]) if args else 0
+    for a, o in zip(args, p.pi):
+        if tuple(a.shape) != (N,) + tuple(o.shape):
+            raise TypeError(f"{p.name}: per-item operand {o.name} has shape {tuple(a.shape)}, expected "
+                            f"{(N,) + tuple(o.shape)}")
+    if N > 2 ** 31 - 1:
+        raise ValueError("tallymap_b200: at most 2^31 - 1 items per call (tallymap/_api.py:540-542)")
+    for x, o in zip(bc, p.bc):
+        t = _dev(x, dev, o.dtype)
+        if tuple(t.shape) != tuple(o.shape):
+            raise TypeError(f"{p.name}: broadcast operand {o.name} has shape {tuple(t.shape)}, expected {o.shape}")
+        args.append(t)
+    args.append(_consts(tuple(int(c) for c in consts) or (0,), dev))
+    layout, n_zero = p.result_layout(N)
+    res = out if out is not None else alloc_results(p, N, dev)
+    kid, nbuf = _lib.kernel_id(p.kernel)
+    ptrs = [t.data_ptr() for t in args] + [t.data_ptr() for t in res]
+    if len(ptrs) != nbuf:
+        raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {p.kernel} takes {nbuf}")
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=4 if p.spawns else 0)
+    names = [n for n, _, _, _ in layout]
+    tallies = [res[names.index(t.name)] for t in p.tallies]
+    ys = res[n_zero:]
+    run.last = dict(ctl=res[names.index("ctl")], args=args)
+    return tallies + [res[names.index("stats")]] + list(ys)
+
+
+_CONSTS = {}
+
+
+def _consts(vals, dev):
+    """the hoisted-constant buffer, made once per (values, device): no host copy on the launch path"""
+    key = (vals, dev.index)
+    t = _CONSTS.get(key)
+    if t is None:
+        t = torch.tensor(vals, dtype=torch.int32).to(dev)
+        _CONSTS[key] = t
+    return t
+
+
+def alloc_results(p, N, device=None):
+    layout, _ = p.result_layout(N)
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    return [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout]
+
+
+def check_status(ctl):
+    """raise if a finished launch's device error word (ctl[3]) is set (a device wait gave up, a bounds check)."""
+    import ctypes
+    w = np.ascontiguousarray(ctl.detach().cpu().numpy().view(np.uint32))
+    _lib.check(_lib.lib().tm_check_status(w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))))

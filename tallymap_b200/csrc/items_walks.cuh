@@ -1,0 +1,331 @@
+// Item programs of the two walker configurations, lowered for the runtime (tm_runtime.cuh): forward and replay
+// adjoint.  Each is the jaxpr of a tallymap item after retrace(cap=max_steps) (tallymap/_rewrite.py:517-528: a
+// counter kc joins the loop, which runs while kc < M && pred; truncated iff kc >= M && pred(out)), with emits as
+// _emit_rule (backends/kernel/kernel.py:984-1003: an index outside [0, S) is dropped and counted in stats[4]).  The
+// adjoints are vjp_prog's (tallymap/_reverse.py:1079-1180): one step VJP per state, the broadcast operand's
+// cotangent summed in f32 newest step first and emitted once per item into an exact tally.
+//
+// Buffer layouts (Params indices; args, then results; the first results up to and including stats are zeroed by the
+// launcher, the layout of backends/kernel/kernel.py:570-591):
+// [per-item inputs] [broadcast inputs, output cotangents] [hoisted constants: i32 max_steps] | results:
+//   q1_fwd   x0 f32[N], keys u32[N,2], theta f32, consts | hist f32[16], ctl u32[8], stats i32[5] | k i32[N], trunc u8[N]
+//   q1_grad  x0, keys, theta, ct_hist f32[16], consts | g_theta f32[1], exact u64[6], ctl, stats | trunc u8[N]
+//   rw_fwd   x0, keys, drift f32, consts | hist f32[256], side f32[2], ctl, stats | k i32[N], trunc u8[N]
+//   rw_grad  x0, keys, drift, ct_hist f32[256], ct_side f32[2], consts | g_drift f32[1], exact u64[6], ctl, stats
+//            | trunc u8[N]
+// (exact: the cotangent tally's 5 carry-save words, then a flag word.)
+#pragma once
+#include "tm_runtime.cuh"
+
+namespace tmb {
+
+// ------------------------------------------------------------------------------------------------ shared pieces
+// a one-bin exact cotangent tally: per-thread register words, merged into the block's shared words, then into the
+// launch's global words; the last block reads it out (kernel.py:625-628: flagged or overflowing -> NaN)
+struct ExactOne {
+  // shared layout: u64 words[5], u32 flag
+  static constexpr int kSmemBytes = 48;
+  __device__ static void flush(ExactPriv<1>& pv, unsigned char* smem, u64* gw, i32* stats, int tid) {
+    u64* const sw = reinterpret_cast<u64*>(smem);
+    u32* const sf = reinterpret_cast<u32*>(smem + 40);
+    if (exact_merge_bin(sw, pv.w[0])) { atomicAdd(&stats[kStFixedPointOverflow], 1); pv.flag |= 1u; }
+    if (pv.flag) atomicOr(sf, 1u);
+    __syncthreads();
+    if (tid == 0) {
+      i64 wv[kExactWords];
+      for (int jj = 0; jj < kExactWords; ++jj) wv[jj] = (i64)sw[jj];
+      bool lost = exact_merge_bin(gw, wv);
+      if (lost) atomicAdd(&stats[kStFixedPointOverflow], 1);
+      if (lost || *sf) atomicOr(reinterpret_cast<u32*>(gw + kExactWords), 1u);
+    }
+  }
+  __device__ static void readout(const u64* gw, float* out, i32* stats) {
+    bool bad = false;
+    const float o = exact_read(gw, &bad);
+    const bool fl = *reinterpret_cast<const u32*>(gw + kExactWords) != 0u;
+    if (bad && !fl) atomicAdd(&stats[kStFixedPointOverflow], 1);
+    *out = (fl || bad) ? __int_as_float(0x7fc00000) : o;
+  }
+};
+
+// a privatised f32 sum tally of S bins at `off` bytes into shared memory: emit (drop + count when out of range) and
+// flush of the nonzero bins with global atomics (kernel.py:681-688)
+template <int S>
+struct SumPriv {
+  __device__ static void emit(float* sh, i32* stats, i32 b, float v) {
+    if ((u32)b >= (u32)S) atomicAdd(&stats[kStDroppedEmits], 1);
+    else fatom(&sh[b], v);
+  }
+  __device__ static void flush(const float* sh, float* g, int tid, int nth) {
+    for (int b = tid; b < S; b += nth) {
+      const float v = sh[b];
+      if (v != 0.0f) fatom(&g[b], v);
+    }
+  }
+};
+
+struct WalkState {
+  i32 kc, k;
+  float x;
+};
+
+// ================================================================================================= Q1 quickstart
+//   body: u = uniform(fold_in(key, k)); t.add("hist", int32(x * 16), theta * (1 - x)); k + 1, x * (0.5 + 0.5 u)
+//   pred: x > 0.05
+struct Q1Common {
+  static constexpr int kNB = 16;
+  __device__ __forceinline__ static bool pred(float x) { return x > 0.05f; }
+};
+
+struct Q1Fwd : Q1Common {
+  enum { kX0, kKeys, kTheta, kConsts, kHist, kCtl, kStats, kK, kTrunc, kNBuf };
+  static constexpr int kSmemBytes = kNB * 4;
+  struct Ctx {
+    const float* x0;
+    const uint2* keys;
+    float theta;
+    i32 M;
+    float* sh;
+    float* hist;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+    Key key;
+  };
+  typedef WalkState State;
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.x0 = static_cast<const float*>(P.p[kX0]);
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.theta = __ldg(static_cast<const float*>(P.p[kTheta]));
+    c.sh = reinterpret_cast<float*>(smem);
+    c.hist = static_cast<float*>(P.p[kHist]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.kout = static_cast<i32*>(P.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    c.key = Key{kk.x, kk.y};
+    return State{0, 0, __ldg(&c.x0[item])};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s) {
+    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.x * 16.0f), c.theta * (1.0f - s.x));
+    s.kc += 1;
+    s.k += 1;
+    s.x = s.x * (0.5f + 0.5f * u);
+  }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item) {
+    c.kout[item] = s.k;
+    c.trunc[item] = (s.kc >= c.M && pred(s.x)) ? 1 : 0;
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.hist, tid, nth);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
+// grad of <ct_hist, hist> w.r.t. theta: the step VJP adds ct_hist[bin] * (1 - x) (0 for a dropped emit,
+// _tally.py:72-82); x does not depend on theta, so it is not an active carry.
+struct Q1Grad : Q1Common {
+  enum { kX0, kKeys, kTheta, kCt, kConsts, kG, kExact, kCtl, kStats, kTrunc, kNBuf };
+  static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
+  struct Ctx {
+    const float* x0;
+    const uint2* keys;
+    i32 M;
+    const float* ct;     // staged in shared memory
+    u64* gw;
+    float* g;
+    i32* stats;
+    uint8_t* trunc;
+    Key key;
+    mutable ExactPriv<1> pv;
+  };
+  typedef WalkState State;
+  struct Adj {
+    float ctb;
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.x0 = static_cast<const float*>(P.p[kX0]);
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.gw = static_cast<u64*>(P.p[kExact]);
+    c.g = static_cast<float*>(P.p[kG]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.ct = reinterpret_cast<const float*>(smem + ExactOne::kSmemBytes);
+    c.pv.zero();
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    const float* ct = static_cast<const float*>(P.p[kCt]);
+    float* d = reinterpret_cast<float*>(smem + ExactOne::kSmemBytes);
+    for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    c.key = Key{kk.x, kk.y};
+    return State{0, 0, __ldg(&c.x0[item])};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
+  __device__ static void adj_start(const Ctx&, Adj& a) { a.ctb = 0.0f; }
+  __device__ __forceinline__ static void micro(const Ctx& c, const State& at, State& next, Adj& a, bool vjp) {
+    const float x = at.x;
+    const i32 k = at.k, kc = at.kc;
+    const float u = uniform01(fold_in(c.key, (u32)k));
+    if (vjp) {
+      const i32 b = f2i(x * 16.0f);
+      const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
+      a.ctb = a.ctb + cv * (1.0f - x);
+    }
+    next = State{kc + 1, k + 1, x * (0.5f + 0.5f * u)};
+  }
+  __device__ static void post_vjp(const Ctx&, const State&, Adj&) {}
+  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {
+    c.trunc[item] = (fin.kc >= c.M && pred(fin.x)) ? 1 : 0;
+    if (c.pv.emit(0, a.ctb)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+  }
+  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
+    ExactOne::flush(c.pv, smem, c.gw, c.stats, tid);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
+    if (tid == 0) ExactOne::readout(c.gw, c.g, c.stats);
+  }
+};
+
+// ================================================================================================= RW 1-D walk
+//   body: u = uniform(fold_in(key, k)); t.add("hist", int32(x * 256), drift * x); k + 1, x + 0.02 * (2u - 1)
+//   pred: 0 <= x <= 1;  after the loop: t.add("side", int32(x > 1), 1.0)
+struct RWCommon {
+  static constexpr int kNB = 256;
+  __device__ __forceinline__ static bool pred(float x) { return x >= 0.0f && x <= 1.0f; }
+  __device__ __forceinline__ static float move(float x, float u) { return x + 0.02f * (2.0f * u - 1.0f); }
+};
+
+struct RWFwd : RWCommon {
+  enum { kX0, kKeys, kDrift, kConsts, kHist, kSide, kCtl, kStats, kK, kTrunc, kNBuf };
+  static constexpr int kSmemBytes = (kNB + 2) * 4;
+  struct Ctx {
+    const float* x0;
+    const uint2* keys;
+    float drift;
+    i32 M;
+    float* sh;
+    float* hist;
+    float* side;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+    Key key;
+  };
+  typedef WalkState State;
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.x0 = static_cast<const float*>(P.p[kX0]);
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.drift = __ldg(static_cast<const float*>(P.p[kDrift]));
+    c.sh = reinterpret_cast<float*>(smem);
+    c.hist = static_cast<float*>(P.p[kHist]);
+    c.side = static_cast<float*>(P.p[kSide]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.kout = static_cast<i32*>(P.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    c.key = Key{kk.x, kk.y};
+    return State{0, 0, __ldg(&c.x0[item])};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s) {
+    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.x * 256.0f), c.drift * s.x);
+    s.kc += 1;
+    s.k += 1;
+    s.x = move(s.x, u);
+  }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item) {
+    SumPriv<2>::emit(c.sh + kNB, c.stats, s.x > 1.0f ? 1 : 0, 1.0f);
+    c.kout[item] = s.k;
+    c.trunc[item] = (s.kc >= c.M && pred(s.x)) ? 1 : 0;
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.hist, tid, nth);
+    SumPriv<2>::flush(reinterpret_cast<const float*>(smem) + kNB, c.side, tid, nth);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
+// grad of <ct_hist, hist> + <ct_side, side> w.r.t. drift: the step VJP adds ct_hist[bin] * x; the side tally does
+// not depend on drift.
+struct RWGrad : RWCommon {
+  enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kG, kExact, kCtl, kStats, kTrunc, kNBuf };
+  static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
+    struct Ctx {
+    const float* x0;
+    const uint2* keys;
+    i32 M;
+    const float* ct;
+    u64* gw;
+    float* g;
+    i32* stats;
+    uint8_t* trunc;
+    Key key;
+    mutable ExactPriv<1> pv;
+  };
+  typedef WalkState State;
+  struct Adj {
+    float ctb;
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.x0 = static_cast<const float*>(P.p[kX0]);
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.gw = static_cast<u64*>(P.p[kExact]);
+    c.g = static_cast<float*>(P.p[kG]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.ct = reinterpret_cast<const float*>(smem + ExactOne::kSmemBytes);
+    c.pv.zero();
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    const float* ct = static_cast<const float*>(P.p[kCtHist]);
+    float* d = reinterpret_cast<float*>(smem + ExactOne::kSmemBytes);
+    for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    c.key = Key{kk.x, kk.y};
+    return State{0, 0, __ldg(&c.x0[item])};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
+  __device__ static void adj_start(const Ctx&, Adj& a) { a.ctb = 0.0f; }
+  __device__ __forceinline__ static void micro(const Ctx& c, const State& at, State& next, Adj& a, bool vjp) {
+    const float x = at.x;
+    const i32 k = at.k, kc = at.kc;
+    const float u = uniform01(fold_in(c.key, (u32)k));
+    if (vjp) {
+      const i32 b = f2i(x * 256.0f);
+      const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
+      a.ctb = a.ctb + cv * x;
+    }
+    next = State{kc + 1, k + 1, move(x, u)};
+  }
+  __device__ static void post_vjp(const Ctx&, const State&, Adj&) {}
+  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {
+    c.trunc[item] = (fin.kc >= c.M && pred(fin.x)) ? 1 : 0;
+    if (c.pv.emit(0, a.ctb)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+  }
+  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
+    ExactOne::flush(c.pv, smem, c.gw, c.stats, tid);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
+    if (tid == 0) ExactOne::readout(c.gw, c.g, c.stats);
+  }
+};
+
+}  // namespace tmb

@@ -1,0 +1,90 @@
+// Auxiliary kernels of the tallymap B200 backend:
+//   exact_combine_kernel   the cross-GPU step of an exact (TSpec.exact) tally: every rank's carry-save words for a
+//                          bin, gathered, are added with their carries and read out once, correctly rounded
+//   exact_scatter_kernel   an exact f32 scatter-add of (value, bin) pairs (the exact Sum accumulator on its own)
+//   probe_threefry_kernel  the calibration probe of the roofline: threefry2x32 evaluations per second at full
+//                          occupancy with no memory traffic (the issue-rate peak of the walkers' dominant op mix)
+#pragma once
+#include "tm_device.cuh"
+
+namespace tmb {
+
+// words: [n_src][n_bins * 5 words, then per-bin u32 flags packed into (n_bins + 1) / 2 u64]: the exact scratch
+// buffers of n_src launches (ranks) laid end to end.  One thread per bin: the bin's words from every source are
+// added with their carries in registers, then read out.  out[b]: the correctly rounded f32, NaN if any source
+// flagged the bin, a carry left the top word, or the total overflows f32 (each counted in stats[3]).
+__global__ void exact_combine_kernel(const u64* words, int n_src, int n_bins, float* out, i32* stats) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n_bins) return;
+  const long long stride = (long long)n_bins * kExactWords + (n_bins + 1) / 2;
+  ExactPriv<1> acc;
+  acc.zero();
+  bool flagged = false, lost = false;
+  for (int r = 0; r < n_src; ++r) {
+    const u64* w = words + r * stride;
+    for (int j = 0; j < kExactWords; ++j) {
+      const i64 q = (i64)w[(long long)b * kExactWords + j];
+      if (q) lost = acc.add_word(0, j, q) || lost;
+    }
+    const u32* fl = reinterpret_cast<const u32*>(w + (long long)n_bins * kExactWords);
+    flagged = flagged || fl[b] != 0u;
+  }
+  if (lost) atomicAdd(&stats[kStFixedPointOverflow], 1);
+  u64 tw[kExactWords];
+  for (int j = 0; j < kExactWords; ++j) tw[j] = (u64)acc.w[0][j];
+  bool bad = false;
+  const float o = exact_read(tw, &bad);
+  if (bad && !flagged && !lost) atomicAdd(&stats[kStFixedPointOverflow], 1);
+  out[b] = (flagged || lost || bad) ? __int_as_float(0x7fc00000) : o;
+}
+
+// exact scatter-add: bins[i] in [0, n_bins) receives vals[i] exactly (out of range: dropped, counted in stats[4]);
+// words / flags in the exact scratch layout above (zeroed by the caller).
+__global__ void exact_scatter_kernel(const float* vals, const i32* bins, long long n, int n_bins, u64* words,
+                                     i32* stats) {
+  u32* const flags = reinterpret_cast<u32*>(words + (long long)n_bins * kExactWords);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const i32 b = bins[i];
+    if ((u32)b >= (u32)n_bins) { atomicAdd(&stats[kStDroppedEmits], 1); continue; }
+    const float v = vals[i];
+    const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
+    bool bad = e == 255u;
+    if (!bad) {
+      const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
+      if (m) {
+        const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
+        const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull), hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
+        const bool neg = (bits >> 31) != 0u;
+        u64* const a = words + (long long)b * kExactWords;
+        if (lo) bad = exact_add_word(a, (int)j, neg ? -lo : lo) || bad;
+        if (hi) bad = exact_add_word(a, (int)j + 1, neg ? -hi : hi) || bad;
+      }
+    }
+    if (bad) { atomicAdd(&stats[kStFixedPointOverflow], 1); atomicOr(&flags[b], 1u); }
+  }
+}
+
+// readout of exact words (layout above) into f32
+__global__ void exact_readout_kernel(const u64* words, int n_bins, float* out, i32* stats) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n_bins) return;
+  const u32* fl = reinterpret_cast<const u32*>(words + (long long)n_bins * kExactWords);
+  bool bad = false;
+  const float o = exact_read(words + (long long)b * kExactWords, &bad);
+  if (bad && !fl[b]) atomicAdd(&stats[kStFixedPointOverflow], 1);
+  out[b] = (fl[b] || bad) ? __int_as_float(0x7fc00000) : o;
+}
+
+// iters independent threefry2x32 evaluations per thread, folded into one word per thread (so none is dead code)
+__global__ void __launch_bounds__(128) probe_threefry_kernel(u32 iters, u32* out) {
+  const u32 t = blockIdx.x * blockDim.x + threadIdx.x;
+  u32 acc = 0u;
+  for (u32 i = 0; i < iters; ++i) {
+    u32 o0, o1;
+    threefry2x32(t, 0x9e3779b9u, 0u, i, o0, o1);
+    acc ^= o0 ^ o1;
+  }
+  out[t] = acc;
+}
+
+}  // namespace tmb

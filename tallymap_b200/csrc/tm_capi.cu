@@ -1,0 +1,313 @@
+// The C ABI of the tallymap B200 backend (include/tallymap_b200.h): kernel registry, launcher, resource query.
+//
+// The reference reaches the device through one XLA FFI handler (tallymap/backends/kernel/shim.cc:157-239) that
+// loads NVRTC modules per context, zeroes the first n_zero results, sizes a persistent grid by occupancy and
+// launches on XLA's stream.  Here the same contract is plain C over the CUDA runtime: built-in kernels are compiled
+// ahead of time for sm_100a into this library; runtime-lowered images are registered as cubins and loaded through
+// the context-independent library API (cudaLibraryLoadData), so no per-context bookkeeping is needed.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/tallymap_b200.h"
+#include "items_walks.cuh"
+#include "tm_aux.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+  return fail(TM_ECUDA, "tallymap_b200: %s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// FNV-1a of a name: the id of a built-in kernel (stable across builds, distinct from registered image ids only by
+// convention: registered ids come from an image digest)
+int64_t name_id(const char* s) {
+  uint64_t h = 1469598103934665603ull;
+  for (; *s; ++s) h = (h ^ (unsigned char)*s) * 1099511628211ull;
+  return (int64_t)(h & 0x7fffffffffffffffull);
+}
+
+struct Kernel {
+  std::string name;
+  const void* fn = nullptr;         // built-in: the __global__ function; registered: the cudaKernel_t
+  int nbuf = 0, smem = 0, block = TM_BLOCK;
+  std::string image, note;          // registered images only
+  cudaLibrary_t lib = nullptr;
+  std::unordered_map<int, int> occ; // device -> resident blocks per SM
+};
+
+std::mutex g_mu;
+std::unordered_map<int64_t, Kernel>* g_reg = nullptr;
+std::vector<std::string>* g_names = nullptr;
+
+template <class I>
+void add_forward(const char* name) {
+  Kernel k;
+  k.name = name;
+  k.fn = reinterpret_cast<const void*>(&tmb::forward_kernel<I>);
+  k.nbuf = I::kNBuf;
+  k.smem = I::kSmemBytes;
+  (*g_reg)[name_id(name)] = k;
+  g_names->push_back(name);
+}
+
+template <class I, int C>
+void add_replay(const char* name) {
+  Kernel k;
+  k.name = name;
+  k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, C>);
+  k.nbuf = I::kNBuf;
+  k.smem = I::kSmemBytes;
+  (*g_reg)[name_id(name)] = k;
+  g_names->push_back(name);
+}
+
+// the built-in programs; the replay adjoints use C = 16 checkpoints (the reference's automatic C for a step of
+// < 1000 equations and a small state, tallymap/_reverse.py:116-134)
+void init_registry() {
+  if (g_reg) return;
+  g_reg = new std::unordered_map<int64_t, Kernel>();
+  g_names = new std::vector<std::string>();
+  add_forward<tmb::Q1Fwd>("q1_fwd");
+  add_replay<tmb::Q1Grad, 16>("q1_grad");
+  add_forward<tmb::RWFwd>("rw_fwd");
+  add_replay<tmb::RWGrad, 16>("rw_grad");
+}
+
+Kernel* find(int64_t id) {
+  init_registry();
+  auto it = g_reg->find(id);
+  return it == g_reg->end() ? nullptr : &it->second;
+}
+
+// load a registered image on first use (library API: valid in every context of the process)
+int ensure_loaded(Kernel& k) {
+  if (k.fn) return TM_OK;
+  cudaError_t e = cudaLibraryLoadData(&k.lib, k.image.data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
+  if (e != cudaSuccess) return cuda_fail("cudaLibraryLoadData", e);
+  cudaKernel_t kern = nullptr;
+  e = cudaLibraryGetKernel(&kern, k.lib, "tm_main");
+  if (e != cudaSuccess) return cuda_fail("cudaLibraryGetKernel(tm_main)", e);
+  k.fn = reinterpret_cast<const void*>(kern);
+  return TM_OK;
+}
+
+int occupancy(Kernel& k, int dev, int* occ) {
+  auto it = k.occ.find(dev);
+  if (it != k.occ.end()) { *occ = it->second; return TM_OK; }
+  if (k.smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+    if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+  }
+  int o = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.block, (size_t)k.smem);
+  if (e != cudaSuccess) return cuda_fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", e);
+  if (o < 1) o = 1;
+  k.occ[dev] = o;
+  *occ = o;
+  return TM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tm_abi_version(void) { return 1; }
+
+const char* tm_last_error(void) { return g_err.c_str(); }
+
+int tm_kernel_id(const char* name, int64_t* id, int32_t* n_buffers) {
+  if (!name || !id) return fail(TM_EINVAL, "tallymap_b200: tm_kernel_id: null argument");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Kernel* k = find(name_id(name));
+  if (!k || k->name != name) return fail(TM_EINVAL, "tallymap_b200: no built-in kernel named '%s'", name);
+  *id = name_id(name);
+  if (n_buffers) *n_buffers = k->nbuf;
+  return TM_OK;
+}
+
+int tm_kernel_name(int32_t i, const char** name) {
+  if (!name) return fail(TM_EINVAL, "tallymap_b200: tm_kernel_name: null argument");
+  std::lock_guard<std::mutex> lk(g_mu);
+  init_registry();
+  *name = (i >= 0 && (size_t)i < g_names->size()) ? (*g_names)[i].c_str() : nullptr;
+  return TM_OK;
+}
+
+int tm_register(int64_t id, const void* image, size_t n, const char* note, int32_t n_buffers, int32_t smem_bytes,
+                int32_t block) {
+  if (!image || n == 0) return fail(TM_EINVAL, "tallymap_b200: tm_register: empty image");
+  if (n_buffers <= 0 || n_buffers > TM_MAXP)
+    return fail(TM_EINVAL, "tallymap_b200: tm_register: %d buffers (1..%d allowed)", n_buffers, TM_MAXP);
+  if (block <= 0 || block > 1024 || block % 32)
+    return fail(TM_EINVAL, "tallymap_b200: tm_register: block %d is not a multiple of 32 in 32..1024", block);
+  std::lock_guard<std::mutex> lk(g_mu);
+  init_registry();
+  Kernel& k = (*g_reg)[id];
+  if (!k.image.empty() || k.fn) return TM_OK;   // first registration wins (shim.cc:134-142)
+  k.name = note ? note : "";
+  k.image.assign(static_cast<const char*>(image), n);
+  k.note = k.name;
+  k.nbuf = n_buffers;
+  k.smem = smem_bytes;
+  k.block = block;
+  return TM_OK;
+}
+
+int tm_kernel_info(int64_t id, long long* out) {
+  if (!out) return fail(TM_EINVAL, "tallymap_b200: tm_kernel_info: null argument");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Kernel* k = find(id);
+  if (!k) return fail(TM_EINVAL, "tallymap_b200: kernel id %lld is not registered", (long long)id);
+  int rc = ensure_loaded(*k);
+  if (rc) return rc;
+  int dev = 0, sms = 0, per_sm = 0, occ = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+  if ((rc = occupancy(*k, dev, &occ))) return rc;
+  cudaFuncAttributes a;
+  e = cudaFuncGetAttributes(&a, k->fn);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncGetAttributes", e);
+  const long long v[7] = {a.numRegs, (long long)a.localSizeBytes, (long long)a.sharedSizeBytes, occ, sms, per_sm,
+                          k->block};
+  for (int i = 0; i < 7; ++i) out[i] = v[i];
+  return TM_OK;
+}
+
+int tm_launch(int64_t id, void* stream, void* const* bufs, int32_t n_args, int32_t n_rets, const size_t* ret_bytes,
+              int32_t n_zero, int32_t flags, int64_t n_items, int32_t* status) {
+  if (status) *status = 0;
+  if (!bufs || (n_rets > 0 && !ret_bytes)) return fail(TM_EINVAL, "tallymap_b200: tm_launch: null buffer list");
+  if (n_items < 0) return fail(TM_EINVAL, "tallymap_b200: tm_launch: n_items %lld < 0", (long long)n_items);
+  if (n_zero < 0 || n_zero > n_rets) return fail(TM_EINVAL, "tallymap_b200: tm_launch: n_zero %d of %d results",
+                                                 n_zero, n_rets);
+  const void* fn;
+  int block, smem, occ, dev = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Kernel* k = find(id);
+    if (!k) return fail(TM_EINVAL, "tallymap_b200: kernel id %lld is not registered in this process", (long long)id);
+    if (n_args + n_rets != k->nbuf)
+      return fail(TM_EINVAL, "tallymap_b200: kernel '%s' takes %d buffers, got %d + %d", k->name.c_str(), k->nbuf,
+                  n_args, n_rets);
+    int rc = ensure_loaded(*k);
+    if (rc) return rc;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+    if ((rc = occupancy(*k, dev, &occ))) return rc;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail("cudaDeviceGetAttribute", e);
+    fn = k->fn;
+    block = k->block;
+    smem = k->smem;
+  }
+  tmb::Params P;
+  std::memset(&P, 0, sizeof(P));
+  for (int i = 0; i < n_args + n_rets; ++i) {
+    if (!bufs[i] && !(i >= n_args && ret_bytes[i - n_args] == 0))
+      return fail(TM_EINVAL, "tallymap_b200: tm_launch: buffer %d is null", i);
+    P.p[i] = bufs[i];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n_zero; ++i) {
+    if (ret_bytes[i] == 0) continue;
+    cudaError_t e = cudaMemsetAsync(bufs[n_args + i], 0, ret_bytes[i], st);
+    if (e != cudaSuccess) {
+      if (status) *status = (int32_t)e;
+      return cuda_fail("cudaMemsetAsync", e);
+    }
+  }
+  if (n_items == 0) return TM_OK;
+  long long grid = (long long)sms * occ;
+  const long long need = (n_items + block - 1) / block;
+  if (grid > need && !(flags & 4)) grid = need;
+  if (grid < 1) grid = 1;
+  long long nn = n_items;
+  void* args[] = {&P, &nn};
+  cudaError_t e = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3((unsigned)block), args, (size_t)smem, st);
+  if (e != cudaSuccess) {
+    if (status) *status = (int32_t)e;
+    return cuda_fail("cudaLaunchKernel", e);
+  }
+  return TM_OK;
+}
+
+int tm_exact_combine(void* stream, const void* words, int32_t n_src, int32_t n_bins, float* out, int32_t* stats) {
+  if (!words || !out || !stats || n_src < 1 || n_bins < 1)
+    return fail(TM_EINVAL, "tallymap_b200: tm_exact_combine: bad arguments");
+  const int blk = 128, grid = (n_bins + blk - 1) / blk;
+  tmb::exact_combine_kernel<<<grid, blk, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const tmb::u64*>(words), n_src, n_bins, out, stats);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TM_OK : cuda_fail("exact_combine_kernel", e);
+}
+
+int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins, void* words,
+                     float* out, int32_t* stats) {
+  if ((n > 0 && (!vals || !bins)) || !words || !out || !stats || n < 0 || n_bins < 1)
+    return fail(TM_EINVAL, "tallymap_b200: tm_exact_scatter: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t wbytes = ((size_t)n_bins * tmb::kExactWords + (n_bins + 1) / 2) * 8;
+  cudaError_t e = cudaMemsetAsync(words, 0, wbytes, st);
+  if (e != cudaSuccess) return cuda_fail("cudaMemsetAsync", e);
+  if (n > 0) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    long long grid = (n + 255) / 256;
+    if (grid > 8LL * sms) grid = 8LL * sms;
+    tmb::exact_scatter_kernel<<<(unsigned)grid, 256, 0, st>>>(vals, bins, n, n_bins, static_cast<tmb::u64*>(words),
+                                                              stats);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("exact_scatter_kernel", e);
+  }
+  tmb::exact_readout_kernel<<<(n_bins + 127) / 128, 128, 0, st>>>(static_cast<const tmb::u64*>(words), n_bins, out,
+                                                                  stats);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TM_OK : cuda_fail("exact_readout_kernel", e);
+}
+
+int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used) {
+  if (!out || iters < 1 || out_len < 128) return fail(TM_EINVAL, "tallymap_b200: tm_probe_threefry: bad arguments");
+  int dev = 0, sms = 0, occ = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, tmb::probe_threefry_kernel, 128, 0);
+  if (e != cudaSuccess) return cuda_fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", e);
+  long long blocks = (long long)sms * (occ < 1 ? 1 : occ);
+  if (blocks * 128 > out_len) blocks = out_len / 128;
+  tmb::probe_threefry_kernel<<<(unsigned)blocks, 128, 0, static_cast<cudaStream_t>(stream)>>>((tmb::u32)iters, out);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("probe_threefry_kernel", e);
+  if (threads_used) *threads_used = blocks * 128;
+  return TM_OK;
+}
+
+int tm_check_status(const uint32_t* ctl_host) {
+  if (!ctl_host) return fail(TM_EINVAL, "tallymap_b200: tm_check_status: null argument");
+  const uint32_t w = ctl_host[tmb::kCtlError];
+  if (w == 0u) return TM_OK;
+  return fail(TM_EDEVICE, "tallymap_b200: device error word 0x%08x (bit 0: a device wait timed out; bit 1: a bounds "
+              "check failed)", w);
+}
+
+}  // extern "C"

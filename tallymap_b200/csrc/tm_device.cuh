@@ -1,0 +1,227 @@
+// Device primitives of the tallymap B200 runtime: scalar types, the kernel parameter block, jax.random's
+// threefry2x32 draws, float->int conversion, the subnormal-safe f32 atomic add and the exact f32 sum.
+//
+// Semantics follow the reference's generated PRELUDE (tallymap/backends/kernel/kernel.py:26-188) and its DENSE
+// accumulator (kernel.py:870-941); the code is written for sm_100a.  All product kernels are compiled with
+// --fmad=false, so every f32 + - * below is one IEEE rounding, as the reference's NVRTC flags (-fmad=false,
+// backends/kernel/compile.py:27) and its host target (-ffp-contract=off) make it.
+#pragma once
+#include <cstdint>
+
+namespace tmb {
+
+typedef int32_t i32;
+typedef uint32_t u32;
+typedef int64_t i64;
+typedef uint64_t u64;
+
+// Kernel parameter block: every buffer pointer of a launch, args first then results (the layout of the reference's
+// SjParams, kernel.py:596 / shim.cc:36-40), passed by value.  TM_MAXP bounds the pointers a program may use.
+#define TM_MAXP 64
+struct Params {
+  void* p[TM_MAXP];
+};
+
+// control words of a launch (one result buffer, u32[8], zeroed by the launcher):
+//   [0..1] item claim counter (u64)   [2] blocks finished (the last one runs the epilogue)   [3] device error word
+//   [4] spawn/queue words or unused ...
+enum { kCtlClaim = 0, kCtlDone = 2, kCtlError = 3, kCtlWords = 8 };
+
+// stats slots (tallymap/_api.py:192-195, kernel.py:594-597): written by number
+enum { kStSpawned = 0, kStChildrenDropped = 1, kStChildrenTruncated = 2, kStFixedPointOverflow = 3, kStDroppedEmits = 4 };
+
+// ------------------------------------------------------------------------------------------------ threefry2x32
+// 20 rounds, rotations 13 15 26 6 / 17 29 16 24, key injection every 4 rounds, k2 = k0 ^ k1 ^ 0x1BD11BDA
+// (kernel.py:137-150; bitwise jax.random's threefry2x32_p).  A rotate is one funnel shift.
+__device__ __forceinline__ u32 rotl(u32 x, int d) { return __funnelshift_l(x, x, d); }
+
+__device__ __forceinline__ void threefry2x32(u32 k0, u32 k1, u32 c0, u32 c1, u32& o0, u32& o1) {
+  const u32 k2 = k0 ^ k1 ^ 0x1BD11BDAu;
+  u32 x0 = c0 + k0, x1 = c1 + k1;
+#define TM_R(r) x0 += x1; x1 = rotl(x1, r); x1 ^= x0;
+  TM_R(13) TM_R(15) TM_R(26) TM_R(6)  x0 += k1; x1 += k2 + 1u;
+  TM_R(17) TM_R(29) TM_R(16) TM_R(24) x0 += k2; x1 += k0 + 2u;
+  TM_R(13) TM_R(15) TM_R(26) TM_R(6)  x0 += k0; x1 += k1 + 3u;
+  TM_R(17) TM_R(29) TM_R(16) TM_R(24) x0 += k1; x1 += k2 + 4u;
+  TM_R(13) TM_R(15) TM_R(26) TM_R(6)  x0 += k2; x1 += k0 + 5u;
+#undef TM_R
+  o0 = x0;
+  o1 = x1;
+}
+
+struct Key {
+  u32 a, b;
+};
+
+// jax.random.fold_in(key, m) = threefry2x32(key, (0, m)) for a 32-bit m (threefry_seed(m) = (0, m))
+__device__ __forceinline__ Key fold_in(Key k, u32 m) {
+  Key o;
+  threefry2x32(k.a, k.b, 0u, m, o.a, o.b);
+  return o;
+}
+
+// random_bits(key, 32, shape)[i] under partitionable threefry: o0 ^ o1 of threefry2x32(key, (0, i))
+__device__ __forceinline__ u32 random_bits32(Key k, u32 i) {
+  u32 o0, o1;
+  threefry2x32(k.a, k.b, 0u, i, o0, o1);
+  return o0 ^ o1;
+}
+
+// the f32 in [0, 1) of jax.random.uniform's mantissa fill: bitcast((bits >> 9) | 0x3f800000) - 1
+__device__ __forceinline__ float bits_to_unit(u32 bits) { return __uint_as_float((bits >> 9) | 0x3f800000u) - 1.0f; }
+
+// jax.random.uniform(key, (), f32) with minval 0, maxval 1.  jax computes max(0, f * (1 - 0) + 0); for f in [0, 1)
+// that is f itself, bitwise (f * 1 = f, f + 0 = f for f >= +0, max(0, f) = f), so the scale and clamp are omitted.
+__device__ __forceinline__ float uniform01(Key k, u32 i = 0u) { return bits_to_unit(random_bits32(k, i)); }
+
+// jax.random.uniform(key, shape, f32, lo, hi)[i]: max(lo, f * (hi - lo) + lo), each op one rounding
+__device__ __forceinline__ float uniform(Key k, u32 i, float lo, float hi) {
+  const float f = bits_to_unit(random_bits32(k, i));
+  const float r = f * (hi - lo) + lo;
+  return (lo > r || lo != lo) ? lo : ((r > lo || r != r) ? r : (lo == 0.0f ? lo + r : lo));
+}
+
+// ------------------------------------------------------------------------------------------------ conversions
+// x.astype(int32): toward zero, saturating, NaN -> 0 (PTX cvt.rzi.s32.f32; the reference's __float2int_rz)
+__device__ __forceinline__ i32 f2i(float x) { return __float2int_rz(x); }
+
+// ------------------------------------------------------------------------------------------------ f32 sum atomics
+// The hardware f32 atomic add flushes subnormal inputs and results to zero.  An add of |v| >= 2^-102 never meets a
+// subnormal (the bin is below half an ulp of v, and v + bin is a multiple of 2^-126 or above it), so it keeps the
+// one-instruction atomic; a smaller nonzero v goes through a compare-and-swap loop of the IEEE add; +-0 changes no
+// bin (kernel.py:112-135, sj_fatom).
+__device__ __forceinline__ void fatom(float* a, float v) {
+  if (v == 0.0f) return;
+  if (!(fabsf(v) < __int_as_float(0x0c800000))) {   // 2^-102
+    atomicAdd(a, v);
+    return;
+  }
+  u32* const u = reinterpret_cast<u32*>(a);
+  u32 o = *reinterpret_cast<volatile u32*>(u), w;
+  do {
+    w = o;
+    o = atomicCAS(u, w, __float_as_uint(__fadd_rn(__uint_as_float(w), v)));
+  } while (o != w);
+}
+
+// ------------------------------------------------------------------------------------------------ exact f32 sum
+// A bin keeps the exact sum of its f32 emits as an integer in units of 2^-149, in kExactWords signed int64 words of
+// weight 2^(63 j) (kernel.py:870-941).  An add into word j that overflows int64 carries +-2 into word j+1; a carry
+// out of the top word returns true and the caller flags the bin (NaN at readout), so a bin is exact or NaN.
+constexpr int kExactWords = 5;
+
+__device__ __noinline__ bool exact_carry(u64* a, int j, i64 c) {   // the rare +-2 carry into word j
+  for (; j < kExactWords; ++j) {
+    const i64 o = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)c);
+    const i64 r = (i64)((u64)o + (u64)c);
+    if (!((c > 0 && r < o) || (c < 0 && r > o))) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool exact_add_word(u64* a, int j, i64 q) {
+  const i64 o = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)q);
+  const i64 r = (i64)((u64)o + (u64)q);
+  if (q > 0 && r < o) return exact_carry(a, j + 1, 2);
+  if (q < 0 && r > o) return exact_carry(a, j + 1, -2);
+  return false;
+}
+
+// A thread-private exact accumulator of NB bins in registers: per-item cotangents are added here without atomics,
+// and each thread adds its words into the block's shared words once, when it runs out of items.  Integer addition
+// is associative, so where a value is added first does not change the total: the readout is bitwise the same as
+// adding every emit straight into the global bin.
+template <int NB>
+struct ExactPriv {
+  i64 w[NB][kExactWords];
+  u32 flag;   // bit b: bin b saw a non-finite emit or lost a carry
+
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int j = 0; j < kExactWords; ++j) w[b][j] = 0;
+    flag = 0u;
+  }
+  // word j of bin b += q (non-atomic), carries rippling upward; true if a carry leaves the top word
+  __device__ __forceinline__ bool add_word(int b, int j, i64 q) {
+    bool lost = false;
+#pragma unroll
+    for (int jj = 0; jj < kExactWords; ++jj) {
+      if (jj < j || q == 0) continue;
+      const i64 o = w[b][jj];
+      const i64 r = (i64)((u64)o + (u64)q);
+      w[b][jj] = r;
+      q = (q > 0 && r < o) ? 2 : ((q < 0 && r > o) ? -2 : 0);
+      j = jj + 1;
+    }
+    if (q != 0) lost = true;
+    return lost;
+  }
+  // add one f32 into bin b; returns true when the bin must be flagged (non-finite, or carry lost)
+  __device__ __forceinline__ bool emit(int b, float v) {
+    const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
+    if (e == 255u) { flag |= 1u << b; return true; }
+    const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
+    if (m == 0ull) return false;
+    const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
+    const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
+    const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
+    const bool neg = (bits >> 31) != 0u;
+    bool lost = false;
+    if (lo) lost = add_word(b, (int)j, neg ? -lo : lo);
+    if (hi) lost = add_word(b, (int)j + 1, neg ? -hi : hi) || lost;
+    if (lost) flag |= 1u << b;
+    return lost;
+  }
+};
+
+// add a thread's private words into exact bins held elsewhere (shared or global): true if a carry was lost
+__device__ __forceinline__ bool exact_merge_bin(u64* dst, const i64* src) {
+  bool lost = false;
+#pragma unroll
+  for (int j = 0; j < kExactWords; ++j)
+    if (src[j]) lost = exact_add_word(dst, j, src[j]) || lost;
+  return lost;
+}
+
+// The correctly rounded (nearest, ties to even) f32 of sum_j a[j] 2^(63 j) 2^-149: the words are summed into a
+// 384-bit two's complement integer, its magnitude's top 64 bits plus a sticky bit are rounded once to 24 bits.
+// *bad: the total overflows f32.
+__device__ __noinline__ float exact_read(const u64* a, bool* bad) {
+  u64 d[6] = {0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
+  for (int j = 0; j < kExactWords; ++j) {
+    const i64 w = (i64)a[j];
+    const int sh = 63 * j, limb = sh >> 6, bit = sh & 63;
+    const u64 ext = w < 0 ? ~0ull : 0ull;
+    const u64 lo = (u64)w << bit, hi = bit ? (u64)(w >> (64 - bit)) : ext;
+    u64 c = 0ull;
+    for (int k = limb; k < 6; ++k) {
+      const u64 y = (k == limb) ? lo : (k == limb + 1 ? hi : ext);
+      const u64 t = d[k] + y, u = t + c;
+      c = (t < y ? 1ull : 0ull) + (u < t ? 1ull : 0ull);
+      d[k] = u;
+    }
+  }
+  const bool neg = (i64)d[5] < 0;
+  if (neg) {
+    u64 c = 1ull;
+    for (int k = 0; k < 6; ++k) { d[k] = ~d[k] + c; c = (c && d[k] == 0ull) ? 1ull : 0ull; }
+  }
+  int t = 5;
+  while (t >= 0 && d[t] == 0ull) --t;
+  if (t < 0) return 0.0f;
+  const int lz = __clzll((long long)d[t]);
+  const u64 below = t >= 1 ? d[t - 1] : 0ull;
+  const u64 top = lz ? (d[t] << lz) | (below >> (64 - lz)) : d[t];
+  bool sticky = lz ? (below << lz) != 0ull : below != 0ull;
+  for (int j = 0; j < t - 1; ++j) sticky = sticky || d[j] != 0ull;
+  u64 q = top >> 40;
+  const u64 rem = top & 0xffffffffffull, half = 0x8000000000ull;
+  if (rem > half || (rem == half && (sticky || (q & 1ull)))) ++q;
+  const float o = (float)ldexp((double)q, 64 * t + 40 - lz - 149);
+  if (!(fabs((double)o) <= 3.4028234663852886e38)) *bad = true;
+  return neg ? -o : o;
+}
+
+}  // namespace tmb
