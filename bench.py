@@ -35,12 +35,11 @@ sys.path.insert(0, ROOT)
 
 N_ITEMS = 4194304
 MAX_STEPS = 20000
-C_CKPT = 16
 TF_OPS = 79          # INT32 ops per threefry2x32 (2 XOR + 2 ADD + 20 x (ADD, ROTL, XOR) + 5 x 3 ADD)
 METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
 CONFIG = {"workload": "1-D random walk (BASELINE config 2): forward + grad w.r.t. drift", "items_per_gpu": N_ITEMS,
           "max_steps": MAX_STEPS, "tally": "Sum((256,)) f32 + Sum((2,)) f32, per-item k int32",
-          "rev_checkpoints": C_CKPT, "l2": "flushed between timed steps (256 MiB write)"}
+          "l2": "flushed between timed steps (256 MiB write)"}
 
 
 def rw_inputs(n, start=0):
@@ -49,7 +48,7 @@ def rw_inputs(n, start=0):
     return prng.uniform(kx, n, start=start), prng.split(ks, n, start=start)
 
 
-def replay_micro_steps(K, C=C_CKPT):
+def replay_micro_steps(K, C):
     """loop-step evaluations of the checkpointed replay (count, checkpoint, advance + fill, sweep) for trip counts K,
     summed: the schedule of tallymap/_reverse.py:343-440."""
     ks, cnt = np.unique(np.asarray(K, np.int64), return_counts=True)
@@ -289,7 +288,10 @@ def main():
     kk = fo[-2].to("cpu").numpy()
     steps_total = int(kk.astype(np.int64).sum())
     tf_fwd = 2 * steps_total
-    tf_grad = 2 * replay_micro_steps(kk)
+    C_used = B.replay_plan(B.RW_GRAD, MAX_STEPS, None, dev)[0]
+    # the replay evaluates forward steps in its count, checkpoint and fill passes (2 threefry2x32 each); its sweep's
+    # step VJPs draw nothing
+    tf_grad = 2 * (replay_micro_steps(kk, C_used) - steps_total)
     import ctypes
     pout = torch.empty(148 * 2048 * 2, dtype=torch.int32, device=dev)
     used = ctypes.c_int64()
@@ -317,7 +319,8 @@ def main():
         "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm on the host, seed 1)",
-        "config": dict(CONFIG, items_total=N * world, parallelism=f"items sharded over {world} GPU(s)"),
+        "config": dict(CONFIG, items_total=N * world, parallelism=f"items sharded over {world} GPU(s)",
+                       rev_checkpoints=C_used),
         "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3),
         "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),
         "grad_mitems_s": round(N * world / (g_ms / 1e3) / 1e6, 3),

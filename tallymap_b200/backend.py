@@ -60,13 +60,15 @@ class ItemProgram:
     ys: Tuple[Operand, ...]
     trunc: int = None
     spawns: bool = False
+    replay_state_bytes: int = 0     # an adjoint: bytes of one stored loop state in its replay scratch
 
     @property
     def n_args(self):
         return len(self.pi) + len(self.bc) + 1
 
-    def result_layout(self, N):
-        """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero."""
+    def result_layout(self, N, replay_bytes=0):
+        """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero.  An adjoint's replay
+        scratch (replay_bytes, from replay_plan) comes last and is not zeroed."""
         out = []
         for t in self.tallies:
             out.append((t.name, t.S * _itemsize(t.dtype), t.dtype, t.shape))
@@ -81,6 +83,9 @@ class ItemProgram:
         for y in self.ys:
             out.append((y.name, N * int(np.prod(y.shape, dtype=np.int64)) * _itemsize(y.dtype), y.dtype,
                         (N,) + tuple(y.shape)))
+        if self.replay_state_bytes:
+            n = max(1, (replay_bytes + 15) // 16)
+            out.append(("replay", n * 16, torch.int32, (n * 4,)))
         return out, n_zero
 
 
@@ -99,16 +104,18 @@ Q1_FWD = ItemProgram("q1_fwd", "q1_fwd", pi=(Operand("x", (), _F32), KEY), bc=(O
                      consts=("max_steps",), tallies=(TSpec("hist", (16,)),),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
 Q1_GRAD = ItemProgram("q1_grad", "q1_grad", pi=(Operand("x", (), _F32), KEY),
-                      bc=(Operand("theta", (), _F32), Operand("ct_hist", (16,), _F32)), consts=("max_steps",),
+                      bc=(Operand("theta", (), _F32), Operand("ct_hist", (16,), _F32)),
+                      consts=("max_steps", "rev_checkpoints", "replay_threads"),
                       tallies=(TSpec("ct_theta", (1,), exact=True),),
-                      ys=(Operand("truncated", (), torch.uint8),), trunc=0)
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=4)
 RW_FWD = ItemProgram("rw_fwd", "rw_fwd", pi=(Operand("x", (), _F32), KEY), bc=(Operand("drift", (), _F32),),
                      consts=("max_steps",), tallies=(TSpec("hist", (256,)), TSpec("side", (2,))),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
 RW_GRAD = ItemProgram("rw_grad", "rw_grad", pi=(Operand("x", (), _F32), KEY),
                       bc=(Operand("drift", (), _F32), Operand("ct_hist", (256,), _F32), Operand("ct_side", (2,), _F32)),
-                      consts=("max_steps",), tallies=(TSpec("ct_drift", (1,), exact=True),),
-                      ys=(Operand("truncated", (), torch.uint8),), trunc=0)
+                      consts=("max_steps", "rev_checkpoints", "replay_threads"),
+                      tallies=(TSpec("ct_drift", (1,), exact=True),),
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=4)
 
 PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD)}
 
@@ -119,7 +126,7 @@ def _host(x):
     a = np.asarray(x)
     if a.dtype == np.uint32:
         a = a.view(np.int32)
-    return np.ascontiguousarray(a)
+    return a if a.flags.c_contiguous else np.ascontiguousarray(a)    # (ascontiguousarray makes 0-d arrays 1-d)
 
 
 def _dev(x, device, dtype):
@@ -134,7 +141,48 @@ def _dev(x, device, dtype):
     return t.to(device, non_blocking=True).contiguous()
 
 
-def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, **_):
+# The replay's checkpoint count C (the reference's rev_checkpoints option, tallymap/_reverse.py:116-134).  Any C gives
+# bitwise the same cotangents; C only trades memory for replay work.  The reference picks C from the logical state
+# size (16 for small steps) and notes that the right rule sizes C against device memory; here C is the smallest power
+# of two covering max_steps, at most REV_C_MAX, halved while the scratch of every resident thread exceeds
+# REV_BUDGET_FRACTION of the free device memory.
+REV_C_MAX = 1024
+REV_BUDGET_FRACTION = 0.25
+
+
+_PLANS = {}
+
+
+def replay_plan(p, max_steps, rev_checkpoints=None, device=None):
+    """-> (C, threads, scratch bytes) of adjoint program p's replay on the current device (decided once per program,
+    device, max_steps and option, so repeated launches keep their C and reuse their buffers)."""
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    key = (p.name, dev, int(max_steps), rev_checkpoints)
+    if key not in _PLANS:
+        _PLANS[key] = _replay_plan(p, max_steps, rev_checkpoints, device)
+    return _PLANS[key]
+
+
+def _replay_plan(p, max_steps, rev_checkpoints, device):
+    kid, _ = _lib.kernel_id(p.kernel)
+    info = _lib.kernel_info(kid)
+    threads = info["sms"] * info["blocks_per_sm"] * info["block"]
+    per = lambda C: (3 * C + 1) * p.replay_state_bytes
+    if rev_checkpoints is not None:
+        C = int(rev_checkpoints)
+        if C < 1:
+            raise ValueError("tallymap_b200: rev_checkpoints must be >= 1")
+    else:
+        C = 1
+        while C < min(int(max_steps), REV_C_MAX):
+            C *= 2
+        free, _ = torch.cuda.mem_get_info(device)
+        while C > 16 and threads * per(C) > REV_BUDGET_FRACTION * free:
+            C //= 2
+    return C, threads, threads * per(C)
+
+
+def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, **_):
     """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
     and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
     as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
@@ -162,9 +210,15 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, **_)
         if tuple(t.shape) != tuple(o.shape):
             raise TypeError(f"{p.name}: broadcast operand {o.name} has shape {tuple(t.shape)}, expected {o.shape}")
         args.append(t)
+    replay_bytes = 0
+    if p.replay_state_bytes:
+        C, threads, replay_bytes = replay_plan(p, consts[0], rev_checkpoints, dev)
+        consts = (int(consts[0]), C, threads)
     args.append(_consts(tuple(int(c) for c in consts) or (0,), dev))
-    layout, n_zero = p.result_layout(N)
-    res = out if out is not None else alloc_results(p, N, dev)
+    layout, n_zero = p.result_layout(N, replay_bytes)
+    res = out if out is not None else alloc_results(p, N, dev, replay_bytes)
+    if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
+        raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
     kid, nbuf = _lib.kernel_id(p.kernel)
     ptrs = [t.data_ptr() for t in args] + [t.data_ptr() for t in res]
     if len(ptrs) != nbuf:
@@ -173,8 +227,8 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, **_)
     _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=4 if p.spawns else 0)
     names = [n for n, _, _, _ in layout]
     tallies = [res[names.index(t.name)] for t in p.tallies]
-    ys = res[n_zero:]
-    run.last = dict(ctl=res[names.index("ctl")], args=args)
+    ys = res[n_zero:n_zero + len(p.ys)]
+    run.last = dict(ctl=res[names.index("ctl")], args=args, consts=consts)
     return tallies + [res[names.index("stats")]] + list(ys)
 
 
@@ -191,9 +245,12 @@ def _consts(vals, dev):
     return t
 
 
-def alloc_results(p, N, device=None):
-    layout, _ = p.result_layout(N)
+def alloc_results(p, N, device=None, replay_bytes=None):
+    """result buffers for N items (an adjoint's replay scratch as planned on `device` unless given)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
+    if replay_bytes is None and p.replay_state_bytes:
+        replay_bytes = replay_plan(p, 2 ** 31 - 1, None, device)[2]
+    layout, _ = p.result_layout(N, replay_bytes or 0)
     return [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout]
 
 

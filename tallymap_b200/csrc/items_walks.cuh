@@ -9,11 +9,14 @@
 // launcher, the layout of backends/kernel/kernel.py:570-591):
 // [per-item inputs] [broadcast inputs, output cotangents] [hoisted constants: i32 max_steps] | results:
 //   q1_fwd   x0 f32[N], keys u32[N,2], theta f32, consts | hist f32[16], ctl u32[8], stats i32[5] | k i32[N], trunc u8[N]
-//   q1_grad  x0, keys, theta, ct_hist f32[16], consts | g_theta f32[1], exact u64[6], ctl, stats | trunc u8[N]
+//   q1_grad  x0, keys, theta, ct_hist f32[16], consts | g_theta f32[1], exact u64[6], ctl, stats | trunc u8[N],
+//            replay scratch
 //   rw_fwd   x0, keys, drift f32, consts | hist f32[256], side f32[2], ctl, stats | k i32[N], trunc u8[N]
 //   rw_grad  x0, keys, drift, ct_hist f32[256], ct_side f32[2], consts | g_drift f32[1], exact u64[6], ctl, stats
-//            | trunc u8[N]
-// (exact: the cotangent tally's 5 carry-save words, then a flag word.)
+//            | trunc u8[N], replay scratch
+// (exact: the cotangent tally's 5 carry-save words, then a flag word.  An adjoint's consts are i32[3]: max_steps,
+// the checkpoint count C, the threads its replay scratch holds; the scratch is (3C + 1) stored states per thread and
+// is not zeroed.)  A walker's stored state is x alone: both loop counters equal the step index.
 #pragma once
 #include "tm_runtime.cuh"
 
@@ -131,7 +134,8 @@ struct Q1Fwd : Q1Common {
 // grad of <ct_hist, hist> w.r.t. theta: the step VJP adds ct_hist[bin] * (1 - x) (0 for a dropped emit,
 // _tally.py:72-82); x does not depend on theta, so it is not an active carry.
 struct Q1Grad : Q1Common {
-  enum { kX0, kKeys, kTheta, kCt, kConsts, kG, kExact, kCtl, kStats, kTrunc, kNBuf };
+  enum { kX0, kKeys, kTheta, kCt, kConsts, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
+  enum { kConstM, kConstC, kConstThreads };
   static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
   struct Ctx {
     const float* x0;
@@ -172,16 +176,21 @@ struct Q1Grad : Q1Common {
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
   __device__ static void adj_start(const Ctx&, Adj& a) { a.ctb = 0.0f; }
-  __device__ __forceinline__ static void micro(const Ctx& c, const State& at, State& next, Adj& a, bool vjp) {
-    const float x = at.x;
-    const i32 k = at.k, kc = at.kc;
-    const float u = uniform01(fold_in(c.key, (u32)k));
-    if (vjp) {
-      const i32 b = f2i(x * 16.0f);
-      const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
-      a.ctb = a.ctb + cv * (1.0f - x);
-    }
-    next = State{kc + 1, k + 1, x * (0.5f + 0.5f * u)};
+  typedef float Stored;
+  __device__ __forceinline__ static Stored store(const State& s) { return s.x; }
+  __device__ __forceinline__ static State restore(const Ctx&, Stored x, i64 step) {
+    return State{(i32)step, (i32)step, x};
+  }
+  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) {
+    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    s.kc += 1;
+    s.k += 1;
+    s.x = s.x * (0.5f + 0.5f * u);
+  }
+  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {
+    const i32 b = f2i(at.x * 16.0f);
+    const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
+    a.ctb = a.ctb + cv * (1.0f - at.x);
   }
   __device__ static void post_vjp(const Ctx&, const State&, Adj&) {}
   __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {
@@ -263,7 +272,8 @@ struct RWFwd : RWCommon {
 // grad of <ct_hist, hist> + <ct_side, side> w.r.t. drift: the step VJP adds ct_hist[bin] * x; the side tally does
 // not depend on drift.
 struct RWGrad : RWCommon {
-  enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kG, kExact, kCtl, kStats, kTrunc, kNBuf };
+  enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
+  enum { kConstM, kConstC, kConstThreads };
   static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
     struct Ctx {
     const float* x0;
@@ -304,16 +314,21 @@ struct RWGrad : RWCommon {
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
   __device__ static void adj_start(const Ctx&, Adj& a) { a.ctb = 0.0f; }
-  __device__ __forceinline__ static void micro(const Ctx& c, const State& at, State& next, Adj& a, bool vjp) {
-    const float x = at.x;
-    const i32 k = at.k, kc = at.kc;
-    const float u = uniform01(fold_in(c.key, (u32)k));
-    if (vjp) {
-      const i32 b = f2i(x * 256.0f);
-      const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
-      a.ctb = a.ctb + cv * x;
-    }
-    next = State{kc + 1, k + 1, move(x, u)};
+  typedef float Stored;
+  __device__ __forceinline__ static Stored store(const State& s) { return s.x; }
+  __device__ __forceinline__ static State restore(const Ctx&, Stored x, i64 step) {
+    return State{(i32)step, (i32)step, x};
+  }
+  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) {
+    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    s.kc += 1;
+    s.k += 1;
+    s.x = move(s.x, u);
+  }
+  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {
+    const i32 b = f2i(at.x * 256.0f);
+    const float cv = ((u32)b < (u32)kNB) ? c.ct[b] : 0.0f;
+    a.ctb = a.ctb + cv * at.x;
   }
   __device__ static void post_vjp(const Ctx&, const State&, Adj&) {}
   __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {

@@ -69,27 +69,27 @@ void add_forward(const char* name) {
   g_names->push_back(name);
 }
 
-template <class I, int C>
+template <class I, int V>
 void add_replay(const char* name) {
   Kernel k;
   k.name = name;
-  k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, C>);
+  k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, V>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
   (*g_reg)[name_id(name)] = k;
   g_names->push_back(name);
 }
 
-// the built-in programs; the replay adjoints use C = 16 checkpoints (the reference's automatic C for a step of
-// < 1000 equations and a small state, tallymap/_reverse.py:116-134)
+// the built-in programs; the replay adjoints apply up to 4 step VJPs per iteration (their checkpoint count C is a
+// launch constant)
 void init_registry() {
   if (g_reg) return;
   g_reg = new std::unordered_map<int64_t, Kernel>();
   g_names = new std::vector<std::string>();
   add_forward<tmb::Q1Fwd>("q1_fwd");
-  add_replay<tmb::Q1Grad, 16>("q1_grad");
+  add_replay<tmb::Q1Grad, 4>("q1_grad");
   add_forward<tmb::RWFwd>("rw_fwd");
-  add_replay<tmb::RWGrad, 16>("rw_grad");
+  add_replay<tmb::RWGrad, 4>("rw_grad");
 }
 
 Kernel* find(int64_t id) {
@@ -224,8 +224,9 @@ int tm_launch(int64_t id, void* stream, void* const* bufs, int32_t n_args, int32
   tmb::Params P;
   std::memset(&P, 0, sizeof(P));
   for (int i = 0; i < n_args + n_rets; ++i) {
-    if (!bufs[i] && !(i >= n_args && ret_bytes[i - n_args] == 0))
-      return fail(TM_EINVAL, "tallymap_b200: tm_launch: buffer %d is null", i);
+    // an empty buffer may be null (no items: no kernel runs; an empty result is never written)
+    const bool empty = i < n_args ? n_items == 0 : ret_bytes[i - n_args] == 0;
+    if (!bufs[i] && !empty) return fail(TM_EINVAL, "tallymap_b200: tm_launch: buffer %d is null", i);
     P.p[i] = bufs[i];
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -22,8 +22,7 @@
 // For the replay kernel additionally:
 //   Adj                                the per-item cotangent accumulators (active carries, broadcast cotangents)
 //   void adj_start(const Ctx&, Adj&)
-//   void micro(const Ctx&, const State& at, State& next, Adj&, bool vjp)   next = step(at); if vjp, also apply the
-//                                      step's VJP at `at` (the forward part is shared by every lane of the warp)
+//   Stored, store, restore, fwd, vjp   the compact stored state and the split step (see replay_kernel)
 //   void post_vjp(const Ctx&, const State& final, Adj&)   cotangents of the loop outputs from the code after it
 //   void adj_finish(const Ctx&, const State& init, const State& final, Adj&, i64 item)   pre-loop VJP, cotangent
 //                                      emits, per-item results (the replay's truncation flag)
@@ -84,18 +83,26 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
   u64* const ctr = reinterpret_cast<u64*>(ctl + kCtlClaim);
   typename I::State x;
   i64 item = 0;
-  bool active = false;
+  bool active = false, alive = true;
+  // warp-uniform loop: a lane with no item left keeps iterating (idle) until its whole warp is done, so the step
+  // body always runs reconverged, every stepping lane of the warp in one pass
   for (;;) {
-    if (!active) {
+    if (alive && !active) {
       const u64 t = claim_item(ctr);
-      if (t >= (u64)n_items) break;
-      item = (i64)t;
-      x = I::start(cx, item);
-      active = true;
+      if (t >= (u64)n_items) {
+        alive = false;
+      } else {
+        item = (i64)t;
+        x = I::start(cx, item);
+        active = true;
+      }
     }
-    if (I::cond(cx, x)) {
+    if (!__any_sync(0xffffffffu, alive)) break;
+    const bool stepping = alive && I::cond(cx, x);
+    __syncwarp();
+    if (stepping) {
       I::step(cx, x);
-    } else {
+    } else if (alive) {
       I::finish(cx, x, item);
       active = false;
     }
@@ -107,16 +114,26 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
 
 // ------------------------------------------------------------------------------------------------ replay kernel
 // The reverse-mode program of an item with one top-level loop: the checkpointed loop of tallymap/_reverse.py:324-444
-// run as a per-lane state machine, one loop step (or one step VJP) per iteration.  Per item:
+// run as a per-lane state machine, one loop step per iteration (or up to V step VJPs).  Per item:
 //   COUNT  the forward pass: the state before step k goes to head[min(k, C)] (slot C is a sink), K = trip count
 //   CKPT   (K > C) replay from the initial state, keeping every m-th state, m = max(C, ceil(K / C))
 //   per segment s = ns-1 .. 0, per sub-chunk u = nsub-1 .. 0 of at most C states:
-//     FILL  advance from checkpoint s by u*C steps, then store the sub-chunk's states in the tape
+//     FILL  advance from checkpoint s by u*C steps, storing the sub-chunk's states in the tape
 //     SWEEP apply the step VJP at each stored state, newest first (the first sub-chunk reads the head)
-// The step VJPs therefore run in the same order, on the same states, as the reference's nested loops, so the
-// cotangents are bitwise the same; only the interleaving across lanes differs.  Lanes in different phases still
-// share the forward step (ITEM::micro), so a warp issues one step body per iteration.
-template <class I, int C>
+// The step VJPs run in the same order, on the same states, as the reference's nested loops, whatever C is, so the
+// cotangents are bitwise the reference's; only the work and the memory depend on C.
+//
+// B200 layout: the head, checkpoint and tape buffers (3C + 1 compact states per resident thread) live in a global
+// scratch buffer, contiguous per thread, so a lane's consecutive stores and loads fill and drain whole sectors; C is
+// a launch constant sized by the host from device memory (up to 1024: an item of K <= C steps is counted and swept
+// with no replay).  A lane in SWEEP applies up to V step VJPs per iteration (a VJP is a few instructions against a
+// forward step's two threefry2x32), so lanes sweeping and lanes stepping share the warp's iterations.
+//
+// ITEM additions for this kernel: Stored (the compact state: the carries a step reads that are not the step index),
+// store(State) -> Stored, restore(Ctx, Stored, i64 step) -> State, fwd(Ctx, State&) (one step, no emits),
+// vjp(Ctx, const State& at, Adj&) (the step VJP at the state before the step); kReplay (the scratch buffer) and the
+// launch constants kConstC (C) and kConstThreads (threads the scratch holds).
+template <class I, int V>
 __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
@@ -127,34 +144,63 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   __syncthreads();
   u32* const ctl = static_cast<u32*>(P.p[I::kCtl]);
   u64* const ctr = reinterpret_cast<u64*>(ctl + kCtlClaim);
+  const i32* const consts = static_cast<const i32*>(P.p[I::kConsts]);
+  const i32 C = __ldg(&consts[I::kConstC]);
+  const i64 cap = __ldg(&consts[I::kConstThreads]);
+  const i64 gtid = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  typedef typename I::Stored S;
+  typedef typename I::State X;
+  // a thread beyond the scratch the host sized (a launch on a device with more resident threads than planned for)
+  // takes no items: the others claim them; the error word records it (bit 1)
+  const bool have = gtid < cap && C >= 1;
+  if (!have) atomicOr(&ctl[kCtlError], 2u);
+  S* const head = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * (3 * (i64)C + 1);
+  S* const ck = head + C + 1;
+  S* const tape = ck + C;
 
   enum { IDLE, COUNT, CKPT, SEG, SUB, FILL, SWEEP, DONE };
-  typename I::State head[C + 1], ck[C], tape[C];
-  typename I::State x, init, fin, at;
+  X x, init, fin;
   typename I::Adj adj;
-  int phase = IDLE;
-  i64 item = 0, k = 0, K = 0, m = 0, ns = 0, s = 0, L = 0, u = 0, LL = 0, j = 0, a = 0, i = 0;
+  int phase = have ? IDLE : -1;   // -1: no work left for this lane
+  // step counts are bounded by max_steps < 2^31 (the cap is an i32 launch constant), so 32-bit bookkeeping
+  i64 item = 0;
+  i32 k = 0, K = 0, m = 0, ns = 0, s = 0, L = 0, u = 0, LL = 0, j = 0, a = 0, i = 0, base = 0;
   bool first = false;
+  // warp-uniform loop: a lane with no work left keeps iterating (idle) until its whole warp is done; after the
+  // (divergent) bookkeeping the warp reconverges, so every lane that steps runs the step body in one pass
   for (;;) {
-    bool vjp = false, stop = false;
-    for (;;) {   // bookkeeping until this lane has a step or a step VJP to evaluate
+    bool vjp = false, stop = phase < 0;
+    while (!stop) {   // bookkeeping until this lane has a step or step VJPs to evaluate
       if (phase == COUNT) {
         if (I::cond(cx, x)) {
-          head[k < C ? k : C] = x;
+          head[k < C ? k : C] = I::store(x);
           ++k;
           break;
         }
         K = k;
         fin = x;
         I::post_vjp(cx, fin, adj);
-        m = K > (i64)C * C ? (K + C - 1) / C : C;
+        m = (i64)K > (i64)C * C ? (K + C - 1) / C : C;
         ns = (K + m - 1) / m;
         if (K == 0) { phase = DONE; continue; }
         if (ns > 1) { x = init; j = 0; phase = CKPT; } else { s = 0; phase = SEG; }
         continue;
       }
+      if (phase == SWEEP) {
+        if (i >= 0) { vjp = true; break; }
+        if (u > 0) { --u; phase = SUB; continue; }
+        if (s > 0) { --s; phase = SEG; continue; }
+        phase = DONE;
+        continue;
+      }
+      if (phase == FILL) {
+        if (a >= u * C) tape[a - u * C] = I::store(x);
+        if (a == u * C + LL - 1) { i = LL - 1; phase = SWEEP; continue; }
+        ++a;
+        break;
+      }
       if (phase == CKPT) {
-        if (j % m == 0) ck[j / m] = x;
+        if (j % m == 0) ck[j / m] = I::store(x);
         if (j == (ns - 1) * m) { s = ns - 1; phase = SEG; continue; }
         ++j;
         break;
@@ -166,30 +212,13 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
         continue;
       }
       if (phase == SUB) {
-        LL = min((i64)C, L - u * C);
+        LL = min(C, L - u * C);
         first = (s == 0 && u == 0);
+        base = s * m + u * C;
         if (first) { i = LL - 1; phase = SWEEP; continue; }
-        x = ck[s];
+        x = I::restore(cx, ck[s], s * m);
         a = 0;
         phase = FILL;
-        continue;
-      }
-      if (phase == FILL) {
-        if (a >= u * C) tape[a - u * C] = x;
-        if (a == u * C + LL - 1) { i = LL - 1; phase = SWEEP; continue; }
-        ++a;
-        break;
-      }
-      if (phase == SWEEP) {
-        if (i >= 0) {
-          at = first ? head[i] : tape[i];
-          --i;
-          vjp = true;
-          break;
-        }
-        if (u > 0) { --u; phase = SUB; continue; }
-        if (s > 0) { --s; phase = SEG; continue; }
-        phase = DONE;
         continue;
       }
       if (phase == DONE) {
@@ -197,23 +226,35 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
         phase = IDLE;
         continue;
       }
-      // IDLE: claim the next item
-      const u64 t = claim_item(ctr);
-      if (t >= (u64)n_items) { stop = true; break; }
-      item = (i64)t;
-      init = I::start(cx, item);
-      x = init;
-      ck[0] = init;
-      k = 0;
-      I::adj_start(cx, adj);
-      phase = COUNT;
+      if (phase == IDLE) {
+        const u64 t = claim_item(ctr);
+        if (t >= (u64)n_items) { phase = -1; stop = true; break; }
+        item = (i64)t;
+        init = I::start(cx, item);
+        x = init;
+        ck[0] = I::store(init);
+        k = 0;
+        I::adj_start(cx, adj);
+        phase = COUNT;
+        continue;
+      }
+      phase = -1;   // no scratch for this thread
+      stop = true;
     }
-    if (stop) break;
+    if (!__any_sync(0xffffffffu, phase >= 0)) break;
+    __syncwarp();
+    if (!stop && !vjp) I::fwd(cx, x);
+    __syncwarp();
     if (vjp) {
-      typename I::State nx;
-      I::micro(cx, at, nx, adj, true);
-    } else {
-      I::micro(cx, x, x, adj, false);
+      // up to V stored states, newest first: the loads issue together, then the VJPs run in order
+      const S* const src = first ? head : tape;
+      S st[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) st[v] = src[i - v >= 0 ? i - v : 0];
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        if (i - v >= 0) I::vjp(cx, I::restore(cx, st[v], base + i - v), adj);
+      i -= V;
     }
   }
   __syncthreads();

@@ -55,9 +55,9 @@ def gpu_rw(x, k, drift, M=20000):
     return dict(hist=hist, side=side, stats=stats, k=kk, trunc=tr.astype(bool))
 
 
-def gpu_rw_grad(x, k, drift, ct_hist, ct_side=None, M=20000):
+def gpu_rw_grad(x, k, drift, ct_hist, ct_side=None, M=20000, C=None):
     ct_side = np.zeros(2, np.float32) if ct_side is None else ct_side
-    out = B.run(B.RW_GRAD, [x, k], [np.float32(drift), ct_hist, ct_side], consts=(M,))
+    out = B.run(B.RW_GRAD, [x, k], [np.float32(drift), ct_hist, ct_side], consts=(M,), rev_checkpoints=C)
     torch.cuda.synchronize()
     B.check_status(B.run.last["ctl"])
     g, stats, tr = [o.cpu().numpy() for o in out]
@@ -142,6 +142,17 @@ def test_rw_grad_bitwise(cuda, orc):
     got = gpu_rw_grad(x, k, 1.0, ct)
     assert same_bits(got["g"], ref["g"])
     assert np.array_equal(got["trunc"], ref["trunc"])
+
+
+@pytest.mark.parametrize("C", [1, 3, 16, 64, 1024])
+def test_rw_grad_checkpoint_invariance(cuda, orc, C):
+    """the replay's checkpoint count changes its work and memory, never the cotangent (the step VJPs run in the same
+    order on the same states): every C is bitwise the oracle's C = 16 replay"""
+    x, k = rw_inputs(8192, seed=4)
+    ct = np.random.default_rng(8).uniform(0.5, 1.5, 256).astype(np.float32)
+    ref = orc.rw_grad(x, k, 1.0, ct, nthreads=0)
+    got = gpu_rw_grad(x, k, 1.0, ct, C=C)
+    assert same_bits(got["g"], ref["g"]) and np.array_equal(got["trunc"], ref["trunc"])
 
 
 def test_rw_edge_inputs(cuda, orc):
