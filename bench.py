@@ -2,7 +2,8 @@
 """Benchmark of the tallymap B200 backend on BASELINE config 2: the 1-D random walk, N = 4,194,304 items per GPU.
 
 One STEP = the forward launch plus the reverse-mode gradient launch (w.r.t. the broadcast `drift`) over the step's
-items: "Mitems/s fwd & grad".  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
+items: "Mitems/s fwd & grad"; the gradient's threads claim items longest first by the forward's trip counts (a
+device argsort inside the step).  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
 second) are synthetic, made with jax.random's algorithm on the host (tallymap_b200.prng).  Weak scaling: each rank
 runs its own 4,194,304 items (a contiguous slice of the global item set) and the partial tallies are combined with
 one NCCL collective step (all_reduce of the f32 / i32 tallies, all_gather + on-device combine of the exact gradient
@@ -184,6 +185,7 @@ def main():
     from tallymap_b200 import _lib
     from tallymap_b200 import backend as B
     from tallymap_b200 import parallel
+    from tallymap_b200.api import longest_first
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -212,7 +214,9 @@ def main():
         return out
 
     def grad():
-        out = B.run(B.RW_GRAD, [x0, keys], [drift, ct_hist, ct_side], consts=(MAX_STEPS,), out=go)
+        # the replay claims items longest first by the forward's trip counts (as value_and_grad does)
+        order = longest_first(fo[-2])
+        out = B.run(B.RW_GRAD, [x0, keys], [drift, ct_hist, ct_side], consts=(MAX_STEPS,), out=go, order=order)
         if world > 1:
             parallel.combine_exact(go[gnames.index("ct_drift.exact")], 1, g_all, go[gnames.index("stats")])
         return out

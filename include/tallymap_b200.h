@@ -6,7 +6,7 @@
  * exports and what its handler does, as plain C: pointers, sizes and a stream, no XLA, JAX or torch types.
  *
  * Buffers: every launch takes ONE array of device pointers, the program's inputs first (per-item operands,
- * broadcast operands, hoisted constants), then its results (sum tallies, scratch accumulators, the control words,
+ * broadcast operands, hoisted constants, the optional item claim order), then its results (sum tallies, scratch accumulators, the control words,
  * stats int32[5], per-item results) -- the order of the reference's SjParams (backends/kernel/kernel.py:570-596).
  * The first n_zero results are zeroed on the stream before the kernel runs (shim.cc:210-219).
  *
@@ -60,7 +60,8 @@ int tm_kernel_info(int64_t id, long long* out);
 /* Launch kernel `id` on `stream` (a cudaStream_t; NULL = the legacy default stream) over n_items items.
  *   bufs[n_args + n_rets]: device pointers, inputs then results; ret_bytes[n_rets]: each result's size in bytes
  *   n_zero: the first n_zero results are zeroed (cudaMemsetAsync on `stream`) before the launch
- *   flags: bit 2 (4): the grid is not capped by n_items (a program that spawns children)
+ *   flags: bit 2 (4): the grid is not capped by n_items (a program that spawns children); bit 3 (8): the last
+ *          argument is the program's optional item claim order (int32[n_items] permutation) and may be NULL
  *   status: optional (may be NULL); receives the cudaError_t of the launch (0: launched)
  * The grid is one persistent block per resident slot (SMs x blocks per SM at the kernel's occupancy), capped at
  * ceil(n_items / block).

@@ -105,7 +105,10 @@ class Mapped:
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
     def value_and_grad(self, *args, wrt, cotangents):
-        """(Result, gradient) of one forward and one replay launch, with the inputs moved to the device once."""
+        """(Result, gradient) of one forward and one replay launch, with the inputs moved to the device once.  The
+        replay claims items longest first by the forward's trip counts (an LPT schedule: the replay of an item costs
+        a known function of its trip count), which balances the threads' work and keeps a warp's lanes in the same
+        replay phase; it changes no result (the cotangent tally is exact, per-item results are indexed by item)."""
         dev = torch.device("cuda", torch.cuda.current_device())
         moved = []
         for a, ax in zip(args, self.fam.in_axes):
@@ -114,9 +117,13 @@ class Mapped:
                 moved.append(t.to(dev, non_blocking=True))
             else:
                 moved.append(a)
-        return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
+        res = self(*moved)
+        order = None
+        if isinstance(res.per_item, torch.Tensor) and res.per_item.dtype == torch.int32:
+            order = longest_first(res.per_item)
+        return res, self.grad(*moved, wrt=wrt, cotangents=cotangents, order=order)
 
-    def grad(self, *args, wrt, cotangents):
+    def grad(self, *args, wrt, cotangents, order=None):
         """d <cotangents, outputs> / d args[wrt] for a broadcast operand `wrt` (argument index): one replay launch.
         cotangents: {output name: array of the output's shape}; missing outputs get zero cotangents."""
         if self.fam.in_axes[wrt] is not None:
@@ -130,10 +137,15 @@ class Mapped:
         for t in self.fam.fwd.tallies:
             c = cotangents.get(t.name)
             cts.append(torch.zeros(t.shape, dtype=t.dtype) if c is None else c)
-        out = B.run(g, pi, list(bc) + cts, consts=(self.max_steps,))
+        out = B.run(g, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
         ct = out[0].reshape(())
         trunc = out[len(g.tallies) + 1 + g.trunc]
         return torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
+
+
+def longest_first(k):
+    """the claim order that runs items with the largest trip counts first (a stable descending sort on device)"""
+    return torch.argsort(k, descending=True, stable=True).to(torch.int32)
 
 
 def vmap(item, outputs, in_axes, max_steps=None):

@@ -64,7 +64,7 @@ class ItemProgram:
 
     @property
     def n_args(self):
-        return len(self.pi) + len(self.bc) + 1
+        return len(self.pi) + len(self.bc) + 2     # + hoisted constants + the optional claim order
 
     def result_layout(self, N, replay_bytes=0):
         """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero.  An adjoint's replay
@@ -182,13 +182,14 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
     return C, threads, threads * per(C)
 
 
-def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, **_):
+def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, order=None, **_):
     """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
     and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
     as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
     of `run.last` (for tm_check_status).  target must be 'cuda' (no CPU fallback, as the reference's kernel
     backend never falls back: _primitive.py:189-194).  out: optional preallocated result buffers (as returned by
-    alloc_results), reused without reallocation."""
+    alloc_results), reused without reallocation.  order: optional int32[N] permutation, the order in which the
+    kernel's threads claim items (e.g. longest first, from a primal call's trip counts); it changes no result."""
     if target != "cuda":
         raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
     if not torch.cuda.is_available():
@@ -215,16 +216,22 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         C, threads, replay_bytes = replay_plan(p, consts[0], rev_checkpoints, dev)
         consts = (int(consts[0]), C, threads)
     args.append(_consts(tuple(int(c) for c in consts) or (0,), dev))
+    if order is not None:
+        order = _dev(order, dev, torch.int32)
+        if tuple(order.shape) != (N,):
+            raise TypeError(f"{p.name}: order has shape {tuple(order.shape)}, expected {(N,)}")
+    args.append(order)
     layout, n_zero = p.result_layout(N, replay_bytes)
     res = out if out is not None else alloc_results(p, N, dev, replay_bytes)
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
     kid, nbuf = _lib.kernel_id(p.kernel)
-    ptrs = [t.data_ptr() for t in args] + [t.data_ptr() for t in res]
+    ptrs = [0 if t is None else t.data_ptr() for t in args] + [t.data_ptr() for t in res]
     if len(ptrs) != nbuf:
         raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {p.kernel} takes {nbuf}")
     st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
-    _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=4 if p.spawns else 0)
+    flags = (4 if p.spawns else 0) | 8
+    _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=flags)
     names = [n for n, _, _, _ in layout]
     tallies = [res[names.index(t.name)] for t in p.tallies]
     ys = res[n_zero:n_zero + len(p.ys)]

@@ -7,16 +7,19 @@
 //
 // Buffer layouts (Params indices; args, then results; the first results up to and including stats are zeroed by the
 // launcher, the layout of backends/kernel/kernel.py:570-591):
-// [per-item inputs] [broadcast inputs, output cotangents] [hoisted constants: i32 max_steps] | results:
-//   q1_fwd   x0 f32[N], keys u32[N,2], theta f32, consts | hist f32[16], ctl u32[8], stats i32[5] | k i32[N], trunc u8[N]
-//   q1_grad  x0, keys, theta, ct_hist f32[16], consts | g_theta f32[1], exact u64[6], ctl, stats | trunc u8[N],
+// [per-item inputs] [broadcast inputs, output cotangents] [hoisted constants: i32 max_steps] [item order] | results:
+//   q1_fwd   x0 f32[N], keys u32[N,2], theta f32, consts, order | hist f32[16], ctl u32[8], stats i32[5] | k i32[N],
+//            trunc u8[N]
+//   q1_grad  x0, keys, theta, ct_hist f32[16], consts, order | g_theta f32[1], exact u64[6], ctl, stats | trunc u8[N],
 //            replay scratch
-//   rw_fwd   x0, keys, drift f32, consts | hist f32[256], side f32[2], ctl, stats | k i32[N], trunc u8[N]
-//   rw_grad  x0, keys, drift, ct_hist f32[256], ct_side f32[2], consts | g_drift f32[1], exact u64[6], ctl, stats
-//            | trunc u8[N], replay scratch
-// (exact: the cotangent tally's 5 carry-save words, then a flag word.  An adjoint's consts are i32[3]: max_steps,
-// the checkpoint count C, the threads its replay scratch holds; the scratch is (3C + 1) stored states per thread and
-// is not zeroed.)  A walker's stored state is x alone: both loop counters equal the step index.
+//   rw_fwd   x0, keys, drift f32, consts, order | hist f32[256], side f32[2], ctl, stats | k i32[N], trunc u8[N]
+//   rw_grad  x0, keys, drift, ct_hist f32[256], ct_side f32[2], consts, order | g_drift f32[1], exact u64[6], ctl,
+//            stats | trunc u8[N], replay scratch
+// order: an optional i32[N] permutation, the order in which items are claimed (null: 0..N-1); it changes which
+// thread runs an item when, never a result.  exact: the cotangent tally's 5 carry-save words, then a flag word.  An
+// adjoint's consts are i32[3]: max_steps, the checkpoint count C, the threads its replay scratch holds; the scratch is
+// (3C + 1) stored states per thread and is not zeroed.  A walker's stored state is x alone: both loop counters equal
+// the step index.
 #pragma once
 #include "tm_runtime.cuh"
 
@@ -81,7 +84,7 @@ struct Q1Common {
 };
 
 struct Q1Fwd : Q1Common {
-  enum { kX0, kKeys, kTheta, kConsts, kHist, kCtl, kStats, kK, kTrunc, kNBuf };
+  enum { kX0, kKeys, kTheta, kConsts, kOrder, kHist, kCtl, kStats, kK, kTrunc, kNBuf };
   static constexpr int kSmemBytes = kNB * 4;
   struct Ctx {
     const float* x0;
@@ -134,7 +137,7 @@ struct Q1Fwd : Q1Common {
 // grad of <ct_hist, hist> w.r.t. theta: the step VJP adds ct_hist[bin] * (1 - x) (0 for a dropped emit,
 // _tally.py:72-82); x does not depend on theta, so it is not an active carry.
 struct Q1Grad : Q1Common {
-  enum { kX0, kKeys, kTheta, kCt, kConsts, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
+  enum { kX0, kKeys, kTheta, kCt, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
   static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
   struct Ctx {
@@ -215,7 +218,7 @@ struct RWCommon {
 };
 
 struct RWFwd : RWCommon {
-  enum { kX0, kKeys, kDrift, kConsts, kHist, kSide, kCtl, kStats, kK, kTrunc, kNBuf };
+  enum { kX0, kKeys, kDrift, kConsts, kOrder, kHist, kSide, kCtl, kStats, kK, kTrunc, kNBuf };
   static constexpr int kSmemBytes = (kNB + 2) * 4;
   struct Ctx {
     const float* x0;
@@ -272,7 +275,7 @@ struct RWFwd : RWCommon {
 // grad of <ct_hist, hist> + <ct_side, side> w.r.t. drift: the step VJP adds ct_hist[bin] * x; the side tally does
 // not depend on drift.
 struct RWGrad : RWCommon {
-  enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
+  enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
   static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
     struct Ctx {

@@ -224,8 +224,9 @@ int tm_launch(int64_t id, void* stream, void* const* bufs, int32_t n_args, int32
   tmb::Params P;
   std::memset(&P, 0, sizeof(P));
   for (int i = 0; i < n_args + n_rets; ++i) {
-    // an empty buffer may be null (no items: no kernel runs; an empty result is never written)
-    const bool empty = i < n_args ? n_items == 0 : ret_bytes[i - n_args] == 0;
+    // an empty buffer may be null (no items: no kernel runs; an empty result is never written), and with flags
+    // bit 3 the last argument (the item claim order) may be null
+    const bool empty = i < n_args ? (n_items == 0 || ((flags & 8) && i == n_args - 1)) : ret_bytes[i - n_args] == 0;
     if (!bufs[i] && !empty) return fail(TM_EINVAL, "tallymap_b200: tm_launch: buffer %d is null", i);
     P.p[i] = bufs[i];
   }

@@ -37,7 +37,7 @@ namespace tmb {
 #endif
 
 // Warp-aggregated claim (kernel.py:732-739): the lanes that need an item this iteration take one contiguous run of
-// the counter between them, one atomic per warp.  -> this lane's item index (>= n_items: nothing left).
+// the counter between them, one atomic per warp.  -> this lane's claim ticket (>= n_items: nothing left).
 __device__ __forceinline__ u64 claim_item(u64* ctr) {
   const unsigned m = __activemask();
   const int lane = threadIdx.x & 31;
@@ -48,6 +48,11 @@ __device__ __forceinline__ u64 claim_item(u64* ctr) {
   base = __shfl_sync(m, base, leader);
   return (u64)base + rank;
 }
+
+// The item a ticket runs: order[t] when the launch gives a claim order (a permutation of 0..N-1, e.g. longest
+// items first from a primal call's trip counts), else t.  The order only moves work between threads and in time:
+// per-item results are written at the item's own index and exact tallies are order-independent.
+__device__ __forceinline__ i64 ticket_item(const i32* order, u64 t) { return order ? (i64)__ldg(&order[t]) : (i64)t; }
 
 // zero the block's privatised tallies
 __device__ __forceinline__ void smem_zero(unsigned char* smem, int bytes) {
@@ -81,6 +86,7 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
   __syncthreads();
   u32* const ctl = static_cast<u32*>(P.p[I::kCtl]);
   u64* const ctr = reinterpret_cast<u64*>(ctl + kCtlClaim);
+  const i32* const order = static_cast<const i32*>(P.p[I::kOrder]);
   typename I::State x;
   i64 item = 0;
   bool active = false, alive = true;
@@ -92,7 +98,7 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
       if (t >= (u64)n_items) {
         alive = false;
       } else {
-        item = (i64)t;
+        item = ticket_item(order, t);
         x = I::start(cx, item);
         active = true;
       }
@@ -145,6 +151,7 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   u32* const ctl = static_cast<u32*>(P.p[I::kCtl]);
   u64* const ctr = reinterpret_cast<u64*>(ctl + kCtlClaim);
   const i32* const consts = static_cast<const i32*>(P.p[I::kConsts]);
+  const i32* const order = static_cast<const i32*>(P.p[I::kOrder]);
   const i32 C = __ldg(&consts[I::kConstC]);
   const i64 cap = __ldg(&consts[I::kConstThreads]);
   const i64 gtid = (i64)blockIdx.x * blockDim.x + threadIdx.x;
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
       if (phase == IDLE) {
         const u64 t = claim_item(ctr);
         if (t >= (u64)n_items) { phase = -1; stop = true; break; }
-        item = (i64)t;
+        item = ticket_item(order, t);
         init = I::start(cx, item);
         x = init;
         ck[0] = I::store(init);

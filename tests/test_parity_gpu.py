@@ -55,9 +55,10 @@ def gpu_rw(x, k, drift, M=20000):
     return dict(hist=hist, side=side, stats=stats, k=kk, trunc=tr.astype(bool))
 
 
-def gpu_rw_grad(x, k, drift, ct_hist, ct_side=None, M=20000, C=None):
+def gpu_rw_grad(x, k, drift, ct_hist, ct_side=None, M=20000, C=None, order=None):
     ct_side = np.zeros(2, np.float32) if ct_side is None else ct_side
-    out = B.run(B.RW_GRAD, [x, k], [np.float32(drift), ct_hist, ct_side], consts=(M,), rev_checkpoints=C)
+    out = B.run(B.RW_GRAD, [x, k], [np.float32(drift), ct_hist, ct_side], consts=(M,), rev_checkpoints=C,
+                order=order)
     torch.cuda.synchronize()
     B.check_status(B.run.last["ctl"])
     g, stats, tr = [o.cpu().numpy() for o in out]
@@ -153,6 +154,24 @@ def test_rw_grad_checkpoint_invariance(cuda, orc, C):
     ref = orc.rw_grad(x, k, 1.0, ct, nthreads=0)
     got = gpu_rw_grad(x, k, 1.0, ct, C=C)
     assert same_bits(got["g"], ref["g"]) and np.array_equal(got["trunc"], ref["trunc"])
+
+
+@pytest.mark.parametrize("how", ["longest_first", "reversed", "random"])
+def test_claim_order_changes_nothing(cuda, orc, how):
+    """an item claim order moves work between threads, never a result: per-item flags at their own index, the
+    exact gradient bitwise"""
+    from tallymap_b200.api import longest_first
+    x, k = rw_inputs(20000, seed=6)
+    f = gpu_rw(x, k, 1.0)
+    order = {"longest_first": longest_first(torch.from_numpy(f["k"])).numpy(),
+             "reversed": np.arange(len(x), dtype=np.int32)[::-1].copy(),
+             "random": np.random.default_rng(0).permutation(len(x)).astype(np.int32)}[how]
+    ref = orc.rw_grad(x, k, 1.0, np.ones(256, np.float32), nthreads=0)
+    got = gpu_rw_grad(x, k, 1.0, np.ones(256, np.float32), order=order)
+    assert same_bits(got["g"], ref["g"]) and np.array_equal(got["trunc"], ref["trunc"])
+    out = B.run(B.RW_FWD, [x, k], [np.float32(1.0)], consts=(20000,), order=order)
+    kk = out[3].cpu().numpy()
+    assert np.array_equal(kk, f["k"])
 
 
 def test_rw_edge_inputs(cuda, orc):
