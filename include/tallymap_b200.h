@@ -85,6 +85,19 @@ int tm_exact_combine(void* stream, const void* words, int32_t n_src, int32_t n_b
 int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins, void* words,
                      float* out, int32_t* stats);
 
+/* tm_exact_scatter without scratch from the caller and without any device allocation.  Some callers cannot
+ * allocate: an XLA FFI handler, whose device memory belongs to XLA's pool (JAX preallocates most of the GPU, and a
+ * cudaMalloc beside it can fail or fragment memory), and any caller on a path that must not block, since cudaMalloc
+ * and cudaFree may synchronise the device.  This variant keeps its scratch words in a fixed device array inside the
+ * library instead, at most 65,536 bins (2.75 MiB, held by every GPU that loads the library until the process exits);
+ * a larger n_bins is rejected with TM_EINVAL.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.  Each call clears
+ * the words it uses, so consecutive calls are independent, but every call shares the one array: calls that can
+ * overlap on the GPU (other streams, other host threads) race and must be serialised by the caller.
+ * (No counterpart in the reference: its handler receives every scratch buffer from XLA.) */
+int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins,
+                             float* out, int32_t* stats);
+
 /* Calibration probe for rooflines: `iters` threefry2x32 evaluations per thread on every resident thread slot of
  * the device (at most out_len threads, a multiple of 128), no memory traffic besides one word per thread.
  * *threads_used receives the thread count.  Time it on `stream` for the device's threefry issue rate.

@@ -126,6 +126,37 @@ int occupancy(Kernel& k, int dev, int* occ) {
   return TM_OK;
 }
 
+// ------------------------------------------------------------------------------------------------ no-alloc scratch
+// Scratch of tm_exact_scatter_noalloc: the exact words of at most TM_NOALLOC_MAX_BINS bins, in a fixed device array
+// that every GPU loading this library holds until the process exits (2.75 MiB).  Host code must not pass the array's
+// name to a kernel (on the host it is a stand-in, not a device address): noalloc_words() looks up its device address
+// once per device, with that device current, and caches it.
+#define TM_NOALLOC_MAX_BINS 65536
+static __device__ __align__(256) unsigned long long
+    g_noalloc_words[(size_t)TM_NOALLOC_MAX_BINS * tmb::kExactWords + (TM_NOALLOC_MAX_BINS + 1) / 2];
+
+#define TM_NOALLOC_MAX_DEVICES 64
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[TM_NOALLOC_MAX_DEVICES] = {};
+
+int noalloc_words(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= TM_NOALLOC_MAX_DEVICES)
+    return fail(TM_EINVAL, "tallymap_b200: device %d is beyond the %d devices the fixed scratch serves", dev,
+                TM_NOALLOC_MAX_DEVICES);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_words);
+    if (e != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(fixed scratch)", e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -268,6 +299,40 @@ int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64
                      float* out, int32_t* stats) {
   if ((n > 0 && (!vals || !bins)) || !words || !out || !stats || n < 0 || n_bins < 1)
     return fail(TM_EINVAL, "tallymap_b200: tm_exact_scatter: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t wbytes = ((size_t)n_bins * tmb::kExactWords + (n_bins + 1) / 2) * 8;
+  cudaError_t e = cudaMemsetAsync(words, 0, wbytes, st);
+  if (e != cudaSuccess) return cuda_fail("cudaMemsetAsync", e);
+  if (n > 0) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    long long grid = (n + 255) / 256;
+    if (grid > 8LL * sms) grid = 8LL * sms;
+    tmb::exact_scatter_kernel<<<(unsigned)grid, 256, 0, st>>>(vals, bins, n, n_bins, static_cast<tmb::u64*>(words),
+                                                              stats);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("exact_scatter_kernel", e);
+  }
+  tmb::exact_readout_kernel<<<(n_bins + 127) / 128, 128, 0, st>>>(static_cast<const tmb::u64*>(words), n_bins, out,
+                                                                  stats);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TM_OK : cuda_fail("exact_readout_kernel", e);
+}
+
+// The exact scatter-add of tm_exact_scatter without a caller-provided scratch buffer and without allocating: for
+// callers that cannot call cudaMalloc (see the header).  Clears the words it needs, then runs the same two kernels on
+// the same stream.  The fixed scratch is shared by every call in the process, so calls whose work overlaps on the
+// GPU (different streams, or devices sharing nothing but the call order) race on it; serialise them.
+int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins,
+                             float* out, int32_t* stats) {
+  if ((n > 0 && (!vals || !bins)) || !out || !stats || n < 0 || n_bins < 1)
+    return fail(TM_EINVAL, "tallymap_b200: tm_exact_scatter_noalloc: bad arguments");
+  if (n_bins > TM_NOALLOC_MAX_BINS)
+    return fail(TM_EINVAL, "tallymap_b200: tm_exact_scatter_noalloc: %d bins exceed its fixed scratch of %d bins; "
+                "use tm_exact_scatter with a caller-provided scratch buffer", n_bins, TM_NOALLOC_MAX_BINS);
+  void* words = nullptr;
+  int rc = noalloc_words(&words);
+  if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t wbytes = ((size_t)n_bins * tmb::kExactWords + (n_bins + 1) / 2) * 8;
   cudaError_t e = cudaMemsetAsync(words, 0, wbytes, st);
