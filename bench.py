@@ -38,15 +38,47 @@ N_ITEMS = 4194304
 MAX_STEPS = 20000
 TF_OPS = 79          # INT32 ops per threefry2x32 (2 XOR + 2 ADD + 20 x (ADD, ROTL, XOR) + 5 x 3 ADD)
 METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
-CONFIG = {"workload": "1-D random walk (BASELINE config 2): forward + grad w.r.t. drift", "items_per_gpu": N_ITEMS,
-          "max_steps": MAX_STEPS, "tally": "Sum((256,)) f32 + Sum((2,)) f32, per-item k int32",
-          "l2": "flushed between timed steps (256 MiB write)"}
 
 
-def rw_inputs(n, start=0):
+def rw_inputs(n, start=0, total=None):
     from tallymap_b200 import prng
     kx, ks = prng.split(prng.PRNGKey(1), 2)
     return prng.uniform(kx, n, start=start), prng.split(ks, n, start=start)
+
+
+def q1_inputs(n, start=0, total=None):
+    from tallymap_b200 import prng
+    total = total or start + n
+    return (np.linspace(0.1, 0.99, total, dtype=np.float32)[start:start + n].copy(),
+            prng.split(prng.PRNGKey(0), n, start=start))
+
+
+def ph_inputs(n, start=0, total=None):
+    from tallymap_b200 import prng
+    return (prng.split(prng.PRNGKey(2), n, start=start),)
+
+
+class Cfg:
+    """one benchmark configuration: programs, inputs, and the threefry2x32 count of a forward step (tf) and of a
+    replay step VJP (tf_vjp)."""
+
+    def __init__(self, name, fwd, grad, inputs, bc, ct, tallies, max_steps, tf, tf_vjp, items, workload):
+        self.name, self.fwd, self.grad, self.inputs, self.bc, self.ct = name, fwd, grad, inputs, bc, ct
+        self.tallies, self.max_steps, self.tf, self.tf_vjp, self.items = tallies, max_steps, tf, tf_vjp, items
+        self.workload = workload
+
+
+def configs(B):
+    return {
+        "rw": Cfg("rw", B.RW_FWD, B.RW_GRAD, rw_inputs, [1.0], [np.ones(256, np.float32), np.zeros(2, np.float32)],
+                  ["hist", "side"], 20000, 2, 0, N_ITEMS,
+                  "1-D random walk (BASELINE config 2): forward + grad w.r.t. drift"),
+        "ph": Cfg("ph", B.PH_FWD, B.PH_GRAD, ph_inputs, [0.1, 10.0], [np.ones((64, 64, 64), np.float32)], ["dep"],
+                  100000, 5, 3, N_ITEMS,
+                  "photon slab (BASELINE config 3): forward + grad w.r.t. (mu_a, mu_s)"),
+        "q1": Cfg("q1", B.Q1_FWD, B.Q1_GRAD, q1_inputs, [2.0], [np.ones(16, np.float32)], ["hist"], 100, 2, 0, 10000,
+                  "quickstart walker (BASELINE config 1): forward + grad w.r.t. theta"),
+    }
 
 
 def replay_micro_steps(K, C):
@@ -116,45 +148,33 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
-def cpu_sample(n_target_s, nthreads, x, k, log=None):
-    """oracle port (the reference CPU kernel target's model, f32 tallies) on a prefix of the items, sized to about
-    n_target_s seconds of fwd + grad: -> (items, seconds, Mitems/s)"""
-    from oracle import oracle
-    n = 4096
-    while True:
-        t0 = time.perf_counter()
-        oracle.rw_fwd(x[:n], k[:n], 1.0, nthreads=nthreads, f64acc=False)
-        oracle.rw_grad(x[:n], k[:n], 1.0, np.ones(256, np.float32), nthreads=nthreads)
-        dt = time.perf_counter() - t0
-        if dt >= n_target_s or n >= len(x):
-            return n, dt, n / dt / 1e6
-        n = min(len(x), max(n * 2, int(n * n_target_s / max(dt, 1e-3) * 0.9)))
-
-
 def reference_arm(args, rank, world):
     if rank != 0:
         return
     from oracle import oracle
     oracle.build()
+    from tallymap_b200 import backend as B
+    cfg = configs(B)[args.config]
     nth = len(os.sched_getaffinity(0))
     os.environ.setdefault("OMP_PROC_BIND", "close")
-    x, k = rw_inputs(N_ITEMS)
-    n, dt, _ = cpu_sample(2.0, nth, x, k)
+    host = cfg.inputs(args.items or cfg.items, 0)
+    n, dt, _ = cpu_rate(cfg, host, 2.0, nth)
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        oracle.rw_fwd(x[:n], k[:n], 1.0, nthreads=nth, f64acc=False)
-        oracle.rw_grad(x[:n], k[:n], 1.0, np.ones(256, np.float32), nthreads=nth)
+        oracle_step(cfg, host, n, nth)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
     v = n / (ms / 1e3) / 1e6
-    sample = f"first {n} of the {N_ITEMS} items per step (fwd + grad), f32 tallies, {nth} OpenMP threads"
+    sample = (f"first {n} of the {len(host[0])} items per step (fwd + grad), the reference host target's model (f32 "
+              f"tallies, libm), {nth} OpenMP threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "Mitems/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm, host)",
-        "config": dict(CONFIG, sample_items=n),
+        "config": {"workload": cfg.workload, "items_per_gpu": len(host[0]), "max_steps": cfg.max_steps,
+                   "sample_items": n},
         "cpu_baseline": {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "Mitems/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (JAX) cannot run on this image (jax is not installed, no network): this is the "
@@ -162,13 +182,41 @@ def reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------------------------------------------ our arm
+def oracle_step(cfg, host, n, nth):
+    """one fwd + grad of the first n items on the host cores: the oracle in the reference host target's mode (f32
+    tallies; libm transcendentals)"""
+    from oracle import oracle
+    if cfg.name == "rw":
+        oracle.rw_fwd(host[0][:n], host[1][:n], 1.0, nthreads=nth, f64acc=False)
+        oracle.rw_grad(host[0][:n], host[1][:n], 1.0, np.ones(256, np.float32), nthreads=nth)
+    elif cfg.name == "q1":
+        oracle.q1_fwd(host[0][:n], host[1][:n], 2.0, nthreads=nth, f64acc=False)
+        oracle.q1_grad(host[0][:n], host[1][:n], 2.0, np.ones(16, np.float32), nthreads=nth)
+    else:
+        oracle.ph_fwd(host[0][:n], nthreads=nth, f64acc=False, libm=True)
+        oracle.ph_grad(host[0][:n], nthreads=nth, libm=True)
+
+
+def cpu_rate(cfg, host, target_s, nth):
+    """-> (items, seconds, Mitems/s) of oracle_step on a prefix of the items sized to about target_s seconds"""
+    n = min(4096, len(host[0]))
+    while True:
+        t0 = time.perf_counter()
+        oracle_step(cfg, host, n, nth)
+        dt = time.perf_counter() - t0
+        if dt >= target_s or n >= len(host[0]):
+            return n, dt, n / dt / 1e6
+        n = min(len(host[0]), max(n * 2, int(n * target_s / max(dt, 1e-3) * 0.9)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--items", type=int, default=N_ITEMS, help="items per GPU")
+    ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1"])
+    ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
@@ -187,38 +235,38 @@ def main():
     from tallymap_b200 import parallel
     from tallymap_b200.api import longest_first
 
+    cfg = configs(B)[args.config]
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    N = args.items
-    start = rank * N
-    x_h, k_h = rw_inputs(N, start)
-    x0 = torch.from_numpy(x_h).to(dev)
-    keys = torch.from_numpy(k_h.view(np.int32)).to(dev)
-    drift = torch.tensor(1.0, device=dev)
-    ct_hist = torch.ones(256, device=dev)
-    ct_side = torch.zeros(2, device=dev)
-    fo = B.alloc_results(B.RW_FWD, N, dev)
-    go = B.alloc_results(B.RW_GRAD, N, dev)
-    g_all = torch.zeros(1, device=dev)
+    N = args.items or cfg.items
+    host = cfg.inputs(N, rank * N, N * world)
+    pi = [torch.from_numpy(h.view(np.int32) if h.dtype == np.uint32 else h).to(dev) for h in host]
+    bc = [torch.tensor(v, dtype=torch.float32, device=dev) for v in cfg.bc]
+    ct = [torch.from_numpy(c).to(dev) for c in cfg.ct]
+    fo = B.alloc_results(cfg.fwd, N, dev)
+    go = B.alloc_results(cfg.grad, N, dev)
+    nb = cfg.grad.tallies[0].S
+    g_all = torch.zeros(nb, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    glayout, _ = B.RW_GRAD.result_layout(N)
-    gnames = [n for n, _, _, _ in glayout]
+    gnames = [n for n, _, _, _ in cfg.grad.result_layout(N)[0]]
+    ntal = len(cfg.fwd.tallies)
 
     def fwd():
-        out = B.run(B.RW_FWD, [x0, keys], [drift], consts=(MAX_STEPS,), out=fo)
+        out = B.run(cfg.fwd, pi, bc, consts=(cfg.max_steps,), out=fo)
         if world > 1:
-            parallel.all_reduce_sums(out[:3])
+            parallel.all_reduce_sums(out[:ntal + 1])
         return out
 
     def grad():
         # the replay claims items longest first by the forward's trip counts (as value_and_grad does)
         order = longest_first(fo[-2])
-        out = B.run(B.RW_GRAD, [x0, keys], [drift, ct_hist, ct_side], consts=(MAX_STEPS,), out=go, order=order)
+        out = B.run(cfg.grad, pi, bc + ct, consts=(cfg.max_steps,), out=go, order=order)
         if world > 1:
-            parallel.combine_exact(go[gnames.index("ct_drift.exact")], 1, g_all, go[gnames.index("stats")])
+            parallel.combine_exact(go[gnames.index(cfg.grad.tallies[0].name + ".exact")], nb, g_all,
+                                   go[gnames.index("stats")])
         return out
 
     for _ in range(args.warmup):
@@ -253,21 +301,23 @@ def main():
     value = N * world / (tot_ms / 1e3) / 1e6
 
     # ---- e2e: the public API from pinned host inputs, H2D + both launches + result read-back timed
-    f = tm.vmap("walk1d", outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None),
-                max_steps=MAX_STEPS)
-    xp = torch.from_numpy(x_h).pin_memory()
-    kp = torch.from_numpy(k_h.view(np.int32)).pin_memory()
-    cts = {"hist": ct_hist}
+    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart"}[cfg.name]
+    F = tm.FAMILIES[fam]
+    f = tm.vmap(fam, outputs={t.name: tm.Sum(t.shape) for t in F.fwd.tallies}, in_axes=F.in_axes,
+                max_steps=cfg.max_steps)
+    pinned = [p.cpu().pin_memory() for p in pi]
+    wrt = tuple(i for i, ax in enumerate(F.in_axes) if ax is None)
+    cts = {t.name: c for t, c in zip(F.fwd.tallies, ct)}
     d2h = [0]
 
     def e2e_step():
-        r, g = f.value_and_grad(xp, kp, drift, wrt=2, cotangents=cts)
-        outs = [r.outputs["hist"], r.outputs["side"], r.stats["n_truncated"].reshape(1), g.reshape(1)]
+        r, g = f.value_and_grad(*pinned, *bc, wrt=wrt if len(wrt) > 1 else wrt[0], cotangents=cts)
+        outs = [r.outputs[t.name] for t in F.fwd.tallies] + [r.stats["n_truncated"].reshape(1), g.reshape(-1)]
         if world > 1:
-            parallel.all_reduce_sums(outs[:3])
-        host = [o.to("cpu") for o in outs]
-        d2h[0] = sum(h.numel() * h.element_size() for h in host)
-        return host
+            parallel.all_reduce_sums(outs[:-1])
+        host_out = [o.to("cpu") for o in outs]
+        d2h[0] = sum(h.numel() * h.element_size() for h in host_out)
+        return host_out
 
     for _ in range(2):
         e2e_step()
@@ -291,11 +341,11 @@ def main():
     # ---- roofline of the dominant kernel: threefry2x32 evaluations per second against the probe's
     kk = fo[-2].to("cpu").numpy()
     steps_total = int(kk.astype(np.int64).sum())
-    tf_fwd = 2 * steps_total
-    C_used = B.replay_plan(B.RW_GRAD, MAX_STEPS, None, dev)[0]
-    # the replay evaluates forward steps in its count, checkpoint and fill passes (2 threefry2x32 each); its sweep's
-    # step VJPs draw nothing
-    tf_grad = 2 * (replay_micro_steps(kk, C_used) - steps_total)
+    tf_fwd = cfg.tf * steps_total
+    C_used = B.replay_plan(cfg.grad, cfg.max_steps, None, dev)[0]
+    # the replay evaluates forward steps in its count, checkpoint and fill passes (cfg.tf threefry2x32 each) and one
+    # step VJP per step (cfg.tf_vjp each)
+    tf_grad = cfg.tf * (replay_micro_steps(kk, C_used) - steps_total) + cfg.tf_vjp * steps_total
     import ctypes
     pout = torch.empty(148 * 2048 * 2, dtype=torch.int32, device=dev)
     used = ctypes.c_int64()
@@ -308,35 +358,38 @@ def main():
         pe[1].record(stream)
     torch.cuda.synchronize()
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
-    dom = ("rw_grad", tf_grad, g_ms) if g_ms >= f_ms else ("rw_fwd", tf_fwd, f_ms)
+    dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nth = len(os.sched_getaffinity(0))
-        n, dt, v = cpu_sample(10.0, nth, x_h, k_h)
+        n, dt, v = cpu_rate(cfg, host, 10.0, nth)
         cpu = {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port",
-               "sample": f"oracle port (reference CPU kernel target model, f32 tallies): fwd + grad of the first {n} "
-                         f"items, {dt:.1f} s on {nth} OpenMP threads"}
-    info = _lib.kernel_info(_lib.kernel_id("rw_grad")[0])
+               "sample": f"oracle port (the reference CPU kernel target's model: f32 tallies, libm): fwd + grad of "
+                         f"the first {n} items, {dt:.1f} s on {nth} OpenMP threads"}
+    info = _lib.kernel_info(_lib.kernel_id(cfg.grad.kernel)[0])
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm on the host, seed 1)",
-        "config": dict(CONFIG, items_total=N * world, parallelism=f"items sharded over {world} GPU(s)",
-                       rev_checkpoints=C_used),
+        "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm on the host)",
+        "config": {"workload": cfg.workload, "items_per_gpu": N, "items_total": N * world,
+                   "max_steps": cfg.max_steps, "rev_checkpoints": C_used,
+                   "parallelism": f"items sharded over {world} GPU(s)",
+                   "l2": "flushed between timed steps (256 MiB write)"},
         "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3),
         "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),
         "grad_mitems_s": round(N * world / (g_ms / 1e3) / 1e6, 3),
         "mean_trip_count": round(steps_total / N, 2),
         "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
-                "h2d_bytes_per_step": int(x_h.nbytes + k_h.nbytes), "d2h_bytes_per_step": int(d2h[0])},
+                "h2d_bytes_per_step": int(sum(h.nbytes for h in host)), "d2h_bytes_per_step": int(d2h[0])},
         "gpu_launches": args.steps * (2 + (1 if world > 1 else 0)),
         "roofline": {"bound": "issue", "kernel": dom[0], "achieved": round(achieved, 2), "peak": round(peak, 2),
                      "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
                      "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
-                     "work": f"{dom[1]} threefry2x32 per launch (2 per loop step; steps from the per-item trip counts)"},
+                     "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, {cfg.tf_vjp} per step "
+                             "VJP; steps from the per-item trip counts and the replay schedule)"},
         "clocks": clk,
         "kernel_resources": info,
     }

@@ -104,6 +104,12 @@ int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bin
  * (No counterpart in the reference, which reports no rooflines.) */
 int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used);
 
+/* The backend's f32 math on the device, elementwise: fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y) (y only for pow).
+ * The item programs use this math on the device and the same code on the host, so the two agree bitwise; this entry
+ * point lets a caller check that.  (The reference has no counterpart: its device math is libdevice, its host math
+ * libm, backends/kernel/kernel.py:29-57, host.py:9-11.) */
+int tm_math_eval(void* stream, int32_t fn, const float* x, const float* y, float* out, int64_t n);
+
 /* Read a finished launch's device error word (ctl[3] of its control-word buffer, host-visible copy `ctl_host`,
  * 8 uint32 words).  Returns TM_OK when it is clear, TM_EDEVICE (with a message) when a device-side wait gave up or
  * a bounds check failed. */

@@ -66,6 +66,9 @@ def lib():
             L.or_q1_grad.argtypes = [i64, P, P, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
             L.or_rw_fwd.argtypes = [i64, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
             L.or_rw_grad.argtypes = [i64, P, P, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
+            L.or_ph_fwd.argtypes = [i64, P, f32, f32, i32, ctypes.c_int, P, P, P, P, ctypes.c_int, ctypes.c_int]
+            L.or_ph_grad.argtypes = [i64, P, f32, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P, ctypes.c_int]
+            L.or_math.argtypes = [ctypes.c_int, P, P, P, i64]
             _LIB = L
     return _LIB
 
@@ -173,3 +176,38 @@ def rw_grad(x0, keys, drift, ct, max_steps=20000, C=16, nthreads=1):
     st = np.zeros(5, np.int32)
     lib().or_rw_grad(n, _p(x0), _p(keys), float(drift), _p(ct), max_steps, C, nthreads, _p(g), _p(tr), _p(st))
     return dict(g=g, trunc=tr.astype(bool), stats=st)
+
+
+def ph_fwd(keys, mu_a=0.1, mu_s=10.0, max_steps=100000, nthreads=0, f64acc=True, libm=False):
+    keys = np.ascontiguousarray(keys, np.uint32)
+    n = len(keys)
+    dep = np.zeros(64 ** 3, np.float32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_ph_fwd(n, _p(keys), mu_a, mu_s, max_steps, nthreads, _p(dep), _p(k), _p(tr), _p(st), int(f64acc),
+                    int(libm))
+    return dict(dep=dep.reshape(64, 64, 64), k=k, trunc=tr.astype(bool), stats=st)
+
+
+def ph_grad(keys, mu_a=0.1, mu_s=10.0, ct=None, max_steps=100000, C=16, nthreads=0, libm=False):
+    keys = np.ascontiguousarray(keys, np.uint32)
+    ct = np.ones(64 ** 3, np.float32) if ct is None else np.ascontiguousarray(ct, np.float32).reshape(-1)
+    n = len(keys)
+    g = np.zeros(2, np.float32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_ph_grad(n, _p(keys), mu_a, mu_s, _p(ct), max_steps, C, nthreads, _p(g), _p(tr), _p(st), int(libm))
+    return dict(g=g, trunc=tr.astype(bool), stats=st)
+
+
+MATH_FN = {"log": 0, "exp": 1, "sin": 2, "cos": 3, "pow": 4}
+
+
+def math(fn, x, y=None):
+    """the backend's shared f32 math evaluated on the host"""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.ascontiguousarray(np.zeros_like(x) if y is None else y, np.float32)
+    out = np.zeros_like(x)
+    lib().or_math(MATH_FN[fn], _p(x), _p(y), _p(out), len(x))
+    return out

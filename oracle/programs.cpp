@@ -10,8 +10,10 @@
 // The item functions are the benchmark configurations written as tallymap items (jax-style pseudo code in each
 // struct's comment).  Exposed through a plain C ABI for ctypes (oracle/oracle.py).
 #include <cstdio>
+#include <type_traits>
 #include <vector>
 
+#include "../tallymap_b200/csrc/tm_math.h"
 #include "oracle_run.h"
 
 using namespace orc;
@@ -198,6 +200,184 @@ struct RWGrad : RWBase {
   void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
 };
 
+// ================================================================================================= PH: photon slab
+// The item of BASELINE config 3 (its jax-style source is in tallymap_b200/csrc/items_photon.cuh, restated here):
+// per step u = uniform(fold_in(key, k), (4,)); s = -log(1 - u0) / mu_t; p += s d; deposit w * mu_a / mu_t at the
+// clipped voxel when p is inside the 64^3 box; w *= albedo; Henyey-Greenstein (g = 0.9) scattering by (cos_t, phi =
+// 2 pi u2); roulette below 1e-3 with survival u3 < 0.1 (w * 10); the loop runs while the photon is inside and alive.
+// Math: SharedMath = the backend's tm_math.h (bitwise with the device: trip counts comparable exactly);
+// LibmMath = the C library, as the reference's host target (host.py:9-11): comparable statistically.
+struct SharedMath {
+  static float log(float x) { return tmm::logf(x); }
+  static void sincos(float x, float* s, float* c) { tmm::sincosf(x, s, c); }
+};
+struct LibmMath {
+  static float log(float x) { return std::log(x); }
+  static void sincos(float x, float* s, float* c) { *s = std::sin(x); *c = std::cos(x); }
+};
+
+struct PhState { i32 kc, k; float px, py, pz, dx, dy, dz, w; bool alive; };
+
+template <class MathT>
+struct PhBase {
+  const u32* keys;
+  float mu_a, mu_s, mu_t, albedo, frac;
+  i32 M;
+  void init(float a, float s) { mu_a = a; mu_s = s; mu_t = a + s; albedo = s / mu_t; frac = a / mu_t; }
+  Key key(i64 i) const { return Key{keys[2 * i], keys[2 * i + 1]}; }
+  static PhState start() { return PhState{0, 0, 32.0f, 32.0f, 0.0f, 0.0f, 0.0f, 1.0f, 1.0f, true}; }
+  static bool in_box(float x) { return x >= 0.0f && x < 64.0f; }
+  static i32 voxel(float x) { return std::min(std::max(f2i_rz(x), 0), 63); }
+  float path(float u0) const { return (-MathT::log(1.0f - u0)) / mu_t; }
+  static void scatter(PhState& s, float u1, float u2) {
+    const float tmp = 0.19f / (0.1f + 1.8f * u1);
+    float cos_t = (1.81f - tmp * tmp) / 1.8f;
+    cos_t = std::fmin(std::fmax(cos_t, -1.0f), 1.0f);
+    const float sin_t = std::sqrt(1.0f - cos_t * cos_t);
+    float sp, cp;
+    MathT::sincos(6.2831855f * u2, &sp, &cp);
+    const float dx = s.dx, dy = s.dy, dz = s.dz;
+    if (std::fabs(dz) > 0.99999f) {
+      s.dx = sin_t * cp;
+      s.dy = sin_t * sp;
+      s.dz = cos_t * (dz > 0.0f ? 1.0f : -1.0f);
+    } else {
+      const float t = std::sqrt(1.0f - dz * dz);
+      s.dx = (sin_t * ((dx * dz) * cp - dy * sp)) / t + dx * cos_t;
+      s.dy = (sin_t * ((dy * dz) * cp + dx * sp)) / t + dy * cos_t;
+      s.dz = ((-sin_t) * cp) * t + dz * cos_t;
+    }
+  }
+  // one step; deposit (flat index, value) reported through dflat / dval (value 0: nothing added)
+  void step(Key kk, PhState& s, i32* dflat, float* dval) const {
+    const Key nk = fold_in(kk, (u32)s.k);
+    const float u0 = uniform_f32(nk, 0u, 0.0f, 1.0f), u1 = uniform_f32(nk, 1u, 0.0f, 1.0f);
+    const float u2 = uniform_f32(nk, 2u, 0.0f, 1.0f), u3 = uniform_f32(nk, 3u, 0.0f, 1.0f);
+    const float sl = path(u0);
+    s.px = s.px + sl * s.dx;
+    s.py = s.py + sl * s.dy;
+    s.pz = s.pz + sl * s.dz;
+    const bool inside = in_box(s.px) && in_box(s.py) && in_box(s.pz);
+    *dflat = (voxel(s.px) * 64 + voxel(s.py)) * 64 + voxel(s.pz);
+    *dval = inside ? s.w * frac : 0.0f;
+    const float w1 = s.w * albedo;
+    scatter(s, u1, u2);
+    const bool low = w1 < 0.001f, survive = u3 < 0.1f;
+    s.w = low ? (survive ? w1 * 10.0f : 0.0f) : w1;
+    s.alive = inside && !(low && !survive);
+    s.kc += 1;
+    s.k += 1;
+  }
+};
+
+// Acc = float: the reference host target (a 1 MiB tally is not privatised, kernel.py:313-324: every deposit is an
+// atomic add into the shared grid).  Acc = double: the checker, with a private f64 grid per thread, flushed once.
+template <class MathT, class Acc>
+struct PhFwd : PhBase<MathT> {
+  Acc* dep;            // [64^3]
+  i32* k_out;
+  uint8_t* trunc;
+  i32* stats;
+  struct Priv { std::vector<double> d; Priv() : d(std::is_same<Acc, double>::value ? 64 * 64 * 64 : 0, 0.0) {} };
+  void item(i64 i, Priv& p) const {
+    const Key kk = this->key(i);
+    PhState s = this->start();
+    while (s.kc < this->M && s.alive) {
+      i32 f;
+      float v;
+      this->step(kk, s, &f, &v);
+      if (v == 0.0f) continue;
+      if (std::is_same<Acc, double>::value) p.d[f] += (double)v;
+      else add_out(&dep[f], (Acc)v);
+    }
+    trunc[i] = (s.kc >= this->M && s.alive) ? 1 : 0;
+    k_out[i] = s.k;
+  }
+  void flush(Priv& p) const {
+    for (size_t f = 0; f < p.d.size(); ++f)
+      if (p.d[f] != 0.0) add_out(&dep[f], (Acc)p.d[f]);
+  }
+};
+
+// reverse mode: see items_photon.cuh for the step VJP and the pre-loop VJP restated here
+template <class MathT>
+struct PhGrad : PhBase<MathT> {
+  const float* ct;     // [64^3]
+  int C;
+  uint8_t* trunc;
+  i32* stats;
+  ExactBins* gbins;
+  Key kk;
+  struct Adj { float ct_w, ct_frac, ct_albedo; };
+  struct Priv { ExactBins b{2}; };
+  bool cond(const PhState& s) const { return s.kc < this->M && s.alive; }
+  PhState step(const PhState& s) const {
+    PhState n = s;
+    i32 f;
+    float v;
+    PhBase<MathT>::step(kk, n, &f, &v);
+    return n;
+  }
+  void vjp_step(const PhState& at, Adj& a) const {
+    const Key nk = fold_in(kk, (u32)at.k);
+    const float u0 = uniform_f32(nk, 0u, 0.0f, 1.0f), u3 = uniform_f32(nk, 3u, 0.0f, 1.0f);
+    const float sl = this->path(u0);
+    const float px = at.px + sl * at.dx, py = at.py + sl * at.dy, pz = at.pz + sl * at.dz;
+    const bool inside = this->in_box(px) && this->in_box(py) && this->in_box(pz);
+    const float w = at.w, w1 = w * this->albedo;
+    const bool low = w1 < 0.001f, survive = u3 < 0.1f;
+    const float ct_w1 = low ? (survive ? a.ct_w * 10.0f : 0.0f) : a.ct_w;
+    a.ct_albedo = a.ct_albedo + ct_w1 * w;
+    const float ct_w = ct_w1 * this->albedo;
+    const i32 flat = (this->voxel(px) * 64 + this->voxel(py)) * 64 + this->voxel(pz);
+    const float cv = inside ? ct[flat] : 0.0f;
+    a.ct_frac = a.ct_frac + cv * w;
+    a.ct_w = ct_w + cv * this->frac;
+  }
+  void item(i64 i, Priv& p) const {
+    PhGrad me = *this;
+    me.kk = this->key(i);
+    Adj a{0.0f, 0.0f, 0.0f};
+    PhState fin;
+    checkpointed_while(me, this->start(), C, a, &fin, [](const PhState&, Adj& ad) { ad.ct_w = 0.0f; });
+    trunc[i] = (fin.kc >= this->M && fin.alive) ? 1 : 0;
+    const float r = 1.0f / (this->mu_t * this->mu_t);
+    const float ct_mu_t = ((-a.ct_frac) * this->mu_a) * r + ((-a.ct_albedo) * this->mu_s) * r;
+    exact_emit_priv(p.b, 0, a.ct_frac / this->mu_t + ct_mu_t, stats);
+    exact_emit_priv(p.b, 1, a.ct_albedo / this->mu_t + ct_mu_t, stats);
+  }
+  void flush(Priv& p) const { exact_flush(p.b, *gbins, 2, stats); }
+};
+
+template <class MathT>
+static void ph_fwd_run(i64 n, const u32* keys, float mu_a, float mu_s, i32 M, int nthreads, float* dep, i32* k_out,
+                       uint8_t* trunc, i32* stats, int f64acc) {
+  if (f64acc) {
+    std::vector<double> d(64 * 64 * 64, 0.0);
+    PhFwd<MathT, double> p;
+    p.keys = keys; p.init(mu_a, mu_s); p.M = M;
+    p.dep = d.data(); p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+    team_run(p, n, nthreads);
+    for (size_t b = 0; b < d.size(); ++b) dep[b] = (float)d[b];
+    return;
+  }
+  PhFwd<MathT, float> p;
+  p.keys = keys; p.init(mu_a, mu_s); p.M = M;
+  p.dep = dep; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+  team_run(p, n, nthreads);
+}
+
+template <class MathT>
+static void ph_grad_run(i64 n, const u32* keys, float mu_a, float mu_s, const float* ct, i32 M, int C, int nthreads,
+                        float* g, uint8_t* trunc, i32* stats) {
+  ExactBins gb(2);
+  PhGrad<MathT> p;
+  p.keys = keys; p.init(mu_a, mu_s); p.M = M; p.ct = ct; p.C = C;
+  p.trunc = trunc; p.stats = stats; p.gbins = &gb;
+  team_run(p, n, nthreads);
+  exact_readout(gb, 2, g, stats);
+}
+
 }  // namespace
 
 // ================================================================================================= C ABI
@@ -304,6 +484,34 @@ int or_rw_grad(i64 n, const float* x0, const u32* keys, float drift, const float
   team_run(p, n, nthreads);
   exact_readout(g, 1, g_drift, stats);
   return 0;
+}
+
+// libm: 0 = the backend's shared math (bitwise with the device), 1 = the C library (the reference host target)
+int or_ph_fwd(i64 n, const u32* keys, float mu_a, float mu_s, i32 max_steps, int nthreads, float* dep, i32* k_out,
+              uint8_t* trunc, i32* stats, int f64acc, int libm) {
+  if (libm) ph_fwd_run<LibmMath>(n, keys, mu_a, mu_s, max_steps, nthreads, dep, k_out, trunc, stats, f64acc);
+  else ph_fwd_run<SharedMath>(n, keys, mu_a, mu_s, max_steps, nthreads, dep, k_out, trunc, stats, f64acc);
+  return 0;
+}
+
+int or_ph_grad(i64 n, const u32* keys, float mu_a, float mu_s, const float* ct, i32 max_steps, int C, int nthreads,
+               float* g, uint8_t* trunc, i32* stats, int libm) {
+  if (libm) ph_grad_run<LibmMath>(n, keys, mu_a, mu_s, ct, max_steps, C, nthreads, g, trunc, stats);
+  else ph_grad_run<SharedMath>(n, keys, mu_a, mu_s, ct, max_steps, C, nthreads, g, trunc, stats);
+  return 0;
+}
+
+// the shared math on the host, elementwise (fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y))
+void or_math(int fn, const float* x, const float* y, float* out, i64 n) {
+  for (i64 i = 0; i < n; ++i) {
+    switch (fn) {
+      case 0: out[i] = tmm::logf(x[i]); break;
+      case 1: out[i] = tmm::expf(x[i]); break;
+      case 2: out[i] = tmm::sinf(x[i]); break;
+      case 3: out[i] = tmm::cosf(x[i]); break;
+      default: out[i] = tmm::powf(x[i], y[i]); break;
+    }
+  }
 }
 
 }  // extern "C"

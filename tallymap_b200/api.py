@@ -45,14 +45,15 @@ class Family:
     its adjoint program; ys: which per-item results the item returns (besides the truncation flag)."""
     name: str
     fwd: B.ItemProgram
-    grads: dict
+    grads: dict          # tuple of broadcast operand indices -> the adjoint program giving their cotangents
     in_axes: tuple
     default_max_steps: int
 
 
 FAMILIES = {
-    "quickstart": Family("quickstart", B.Q1_FWD, {0: B.Q1_GRAD}, (0, 0, None), 100),
-    "walk1d": Family("walk1d", B.RW_FWD, {0: B.RW_GRAD}, (0, 0, None), 20000),
+    "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100),
+    "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000),
+    "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
 }
 
 
@@ -124,23 +125,30 @@ class Mapped:
         return res, self.grad(*moved, wrt=wrt, cotangents=cotangents, order=order)
 
     def grad(self, *args, wrt, cotangents, order=None):
-        """d <cotangents, outputs> / d args[wrt] for a broadcast operand `wrt` (argument index): one replay launch.
-        cotangents: {output name: array of the output's shape}; missing outputs get zero cotangents."""
-        if self.fam.in_axes[wrt] is not None:
+        """d <cotangents, outputs> / d args[wrt] for broadcast operand(s) `wrt` (an argument index or a tuple of
+        them): ONE replay launch.  cotangents: {output name: array of the output's shape}; missing outputs get zero
+        cotangents.  -> a scalar for one index, a vector for a tuple; NaN when an item's replay hit max_steps."""
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if any(self.fam.in_axes[w] is not None for w in idx):
             raise ValueError("tallymap_b200: grad with respect to a per-item operand is not built for this item")
-        bidx = sum(1 for ax in self.fam.in_axes[:wrt] if ax is None)
-        if bidx not in self.fam.grads:
-            raise NotImplementedError(f"tallymap_b200: item {self.fam.name!r} has no adjoint for argument {wrt}")
+        bpos = tuple(sum(1 for ax in self.fam.in_axes[:w] if ax is None) for w in idx)
+        prog, sel = None, None
+        for key, g in self.fam.grads.items():
+            if all(b in key for b in bpos):
+                prog, sel = g, [key.index(b) for b in bpos]
+                break
+        if prog is None:
+            raise NotImplementedError(f"tallymap_b200: item {self.fam.name!r} has no adjoint for arguments {idx}")
         pi, bc = self._split(args)
-        g = self.fam.grads[bidx]
         cts = []
         for t in self.fam.fwd.tallies:
             c = cotangents.get(t.name)
             cts.append(torch.zeros(t.shape, dtype=t.dtype) if c is None else c)
-        out = B.run(g, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
-        ct = out[0].reshape(())
-        trunc = out[len(g.tallies) + 1 + g.trunc]
-        return torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
+        ct = out[0].reshape(-1)[sel]
+        trunc = out[len(prog.tallies) + 1 + prog.trunc]
+        ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
+        return ct.reshape(()) if isinstance(wrt, int) else ct
 
 
 def longest_first(k):

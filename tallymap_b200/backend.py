@@ -31,6 +31,7 @@ class TSpec:
     shape: Tuple[int, ...]
     dtype: torch.dtype = torch.float32
     exact: bool = False
+    f64: bool = False      # accumulated in an f64 shadow (a scratch result), rounded once to the f32 output
 
     @property
     def S(self):
@@ -73,6 +74,8 @@ class ItemProgram:
         for t in self.tallies:
             out.append((t.name, t.S * _itemsize(t.dtype), t.dtype, t.shape))
         for t in self.tallies:
+            if t.f64:
+                out.append((t.name + ".f64", t.S * 8, torch.float64, (t.S,)))
             if t.exact:
                 # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
                 n64 = t.S * EXACT_WORDS + (t.S + 1) // 2
@@ -117,7 +120,17 @@ RW_GRAD = ItemProgram("rw_grad", "rw_grad", pi=(Operand("x", (), _F32), KEY),
                       tallies=(TSpec("ct_drift", (1,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=4)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD)}
+# BASELINE config 3, the photon slab (csrc/items_photon.cuh)
+PH_FWD = ItemProgram("ph_fwd", "ph_fwd", pi=(KEY,), bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32)),
+                     consts=("max_steps",), tallies=(TSpec("dep", (64, 64, 64), f64=True),),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
+PH_GRAD = ItemProgram("ph_grad", "ph_grad", pi=(KEY,),
+                      bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32), Operand("ct_dep", (64, 64, 64), _F32)),
+                      consts=("max_steps", "rev_checkpoints", "replay_threads"),
+                      tallies=(TSpec("ct_mu", (2,), exact=True),),
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=28)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD)}
 
 
 # -------------------------------------------------------------------------------------------------- run

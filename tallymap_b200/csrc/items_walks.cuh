@@ -21,54 +21,9 @@
 // (3C + 1) stored states per thread and is not zeroed.  A walker's stored state is x alone: both loop counters equal
 // the step index.
 #pragma once
-#include "tm_runtime.cuh"
+#include "tm_tally.cuh"
 
 namespace tmb {
-
-// ------------------------------------------------------------------------------------------------ shared pieces
-// a one-bin exact cotangent tally: per-thread register words, merged into the block's shared words, then into the
-// launch's global words; the last block reads it out (kernel.py:625-628: flagged or overflowing -> NaN)
-struct ExactOne {
-  // shared layout: u64 words[5], u32 flag
-  static constexpr int kSmemBytes = 48;
-  __device__ static void flush(ExactPriv<1>& pv, unsigned char* smem, u64* gw, i32* stats, int tid) {
-    u64* const sw = reinterpret_cast<u64*>(smem);
-    u32* const sf = reinterpret_cast<u32*>(smem + 40);
-    if (exact_merge_bin(sw, pv.w[0])) { atomicAdd(&stats[kStFixedPointOverflow], 1); pv.flag |= 1u; }
-    if (pv.flag) atomicOr(sf, 1u);
-    __syncthreads();
-    if (tid == 0) {
-      i64 wv[kExactWords];
-      for (int jj = 0; jj < kExactWords; ++jj) wv[jj] = (i64)sw[jj];
-      bool lost = exact_merge_bin(gw, wv);
-      if (lost) atomicAdd(&stats[kStFixedPointOverflow], 1);
-      if (lost || *sf) atomicOr(reinterpret_cast<u32*>(gw + kExactWords), 1u);
-    }
-  }
-  __device__ static void readout(const u64* gw, float* out, i32* stats) {
-    bool bad = false;
-    const float o = exact_read(gw, &bad);
-    const bool fl = *reinterpret_cast<const u32*>(gw + kExactWords) != 0u;
-    if (bad && !fl) atomicAdd(&stats[kStFixedPointOverflow], 1);
-    *out = (fl || bad) ? __int_as_float(0x7fc00000) : o;
-  }
-};
-
-// a privatised f32 sum tally of S bins at `off` bytes into shared memory: emit (drop + count when out of range) and
-// flush of the nonzero bins with global atomics (kernel.py:681-688)
-template <int S>
-struct SumPriv {
-  __device__ static void emit(float* sh, i32* stats, i32 b, float v) {
-    if ((u32)b >= (u32)S) atomicAdd(&stats[kStDroppedEmits], 1);
-    else fatom(&sh[b], v);
-  }
-  __device__ static void flush(const float* sh, float* g, int tid, int nth) {
-    for (int b = tid; b < S; b += nth) {
-      const float v = sh[b];
-      if (v != 0.0f) fatom(&g[b], v);
-    }
-  }
-};
 
 struct WalkState {
   i32 kc, k;
@@ -139,7 +94,7 @@ struct Q1Fwd : Q1Common {
 struct Q1Grad : Q1Common {
   enum { kX0, kKeys, kTheta, kCt, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
-  static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
+  static constexpr int kSmemBytes = ExactBins<1>::kSmemBytes + kNB * 4;
   struct Ctx {
     const float* x0;
     const uint2* keys;
@@ -164,12 +119,12 @@ struct Q1Grad : Q1Common {
     c.g = static_cast<float*>(P.p[kG]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
-    c.ct = reinterpret_cast<const float*>(smem + ExactOne::kSmemBytes);
+    c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
     c.pv.zero();
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCt]);
-    float* d = reinterpret_cast<float*>(smem + ExactOne::kSmemBytes);
+    float* d = reinterpret_cast<float*>(smem + ExactBins<1>::kSmemBytes);
     for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
   }
   __device__ static State start(Ctx& c, i64 item) {
@@ -201,10 +156,10 @@ struct Q1Grad : Q1Common {
     if (c.pv.emit(0, a.ctb)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
   }
   __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
-    ExactOne::flush(c.pv, smem, c.gw, c.stats, tid);
+    ExactBins<1>::flush(c.pv, smem, c.gw, c.stats, tid);
   }
   __device__ static void epilogue(const Ctx& c, int tid, int) {
-    if (tid == 0) ExactOne::readout(c.gw, c.g, c.stats);
+    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
   }
 };
 
@@ -277,7 +232,7 @@ struct RWFwd : RWCommon {
 struct RWGrad : RWCommon {
   enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
-  static constexpr int kSmemBytes = ExactOne::kSmemBytes + kNB * 4;
+  static constexpr int kSmemBytes = ExactBins<1>::kSmemBytes + kNB * 4;
     struct Ctx {
     const float* x0;
     const uint2* keys;
@@ -302,12 +257,12 @@ struct RWGrad : RWCommon {
     c.g = static_cast<float*>(P.p[kG]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
-    c.ct = reinterpret_cast<const float*>(smem + ExactOne::kSmemBytes);
+    c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
     c.pv.zero();
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCtHist]);
-    float* d = reinterpret_cast<float*>(smem + ExactOne::kSmemBytes);
+    float* d = reinterpret_cast<float*>(smem + ExactBins<1>::kSmemBytes);
     for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
   }
   __device__ static State start(Ctx& c, i64 item) {
@@ -339,10 +294,10 @@ struct RWGrad : RWCommon {
     if (c.pv.emit(0, a.ctb)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
   }
   __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
-    ExactOne::flush(c.pv, smem, c.gw, c.stats, tid);
+    ExactBins<1>::flush(c.pv, smem, c.gw, c.stats, tid);
   }
   __device__ static void epilogue(const Ctx& c, int tid, int) {
-    if (tid == 0) ExactOne::readout(c.gw, c.g, c.stats);
+    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
   }
 };
 

@@ -6,6 +6,7 @@
 //                          occupancy with no memory traffic (the issue-rate peak of the walkers' dominant op mix)
 #pragma once
 #include "tm_device.cuh"
+#include "tm_math.h"
 
 namespace tmb {
 
@@ -73,6 +74,22 @@ __global__ void exact_readout_kernel(const u64* words, int n_bins, float* out, i
   const float o = exact_read(words + (long long)b * kExactWords, &bad);
   if (bad && !fl[b]) atomicAdd(&stats[kStFixedPointOverflow], 1);
   out[b] = (fl[b] || bad) ? __int_as_float(0x7fc00000) : o;
+}
+
+// the backend's f32 math on the device, elementwise (fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y))
+__global__ void math_eval_kernel(int fn, const float* x, const float* y, float* out, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float a = x[i];
+    float r;
+    switch (fn) {
+      case 0: r = tmm::logf(a); break;
+      case 1: r = tmm::expf(a); break;
+      case 2: r = tmm::sinf(a); break;
+      case 3: r = tmm::cosf(a); break;
+      default: r = tmm::powf(a, y[i]); break;
+    }
+    out[i] = r;
+  }
 }
 
 // iters independent threefry2x32 evaluations per thread, folded into one word per thread (so none is dead code)

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/tallymap_b200.h"
+#include "items_photon.cuh"
 #include "items_walks.cuh"
 #include "tm_aux.cuh"
 
@@ -90,6 +91,8 @@ void init_registry() {
   add_replay<tmb::Q1Grad, 4>("q1_grad");
   add_forward<tmb::RWFwd>("rw_fwd");
   add_replay<tmb::RWGrad, 4>("rw_grad");
+  add_forward<tmb::PHFwd>("ph_fwd");
+  add_replay<tmb::PHGrad, 1>("ph_grad");
 }
 
 Kernel* find(int64_t id) {
@@ -367,6 +370,17 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("probe_threefry_kernel", e);
   if (threads_used) *threads_used = blocks * 128;
   return TM_OK;
+}
+
+int tm_math_eval(void* stream, int32_t fn, const float* x, const float* y, float* out, int64_t n) {
+  if (fn < 0 || fn > 4 || n < 0 || (n > 0 && (!x || !out || (fn == 4 && !y))))
+    return fail(TM_EINVAL, "tallymap_b200: tm_math_eval: bad arguments");
+  if (n == 0) return TM_OK;
+  long long grid = (n + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  tmb::math_eval_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(fn, x, y, out, n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TM_OK : cuda_fail("math_eval_kernel", e);
 }
 
 int tm_check_status(const uint32_t* ctl_host) {
