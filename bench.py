@@ -53,6 +53,17 @@ def q1_inputs(n, start=0, total=None):
             prng.split(prng.PRNGKey(0), n, start=start))
 
 
+def od_inputs(n, start=0, total=None):
+    """sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2) (numpy default_rng(3), as the
+    reference's benchmarks make host inputs), item_id = the global item index"""
+    total = total or start + n
+    rng = np.random.default_rng(3)
+    sigma = rng.uniform(9, 11, total).astype(np.float32)[start:start + n]
+    rho = rng.uniform(26, 30, total).astype(np.float32)[start:start + n]
+    y0 = (1.0 + 0.1 * rng.standard_normal((total, 3))).astype(np.float32)[start:start + n]
+    return sigma.copy(), rho.copy(), y0.copy(), np.arange(start, start + n, dtype=np.int32)
+
+
 def ph_inputs(n, start=0, total=None):
     from tallymap_b200 import prng
     return (prng.split(prng.PRNGKey(2), n, start=start),)
@@ -78,6 +89,9 @@ def configs(B):
                   "photon slab (BASELINE config 3): forward + grad w.r.t. (mu_a, mu_s)"),
         "q1": Cfg("q1", B.Q1_FWD, B.Q1_GRAD, q1_inputs, [2.0], [np.ones(16, np.float32)], ["hist"], 100, 2, 0, 10000,
                   "quickstart walker (BASELINE config 1): forward + grad w.r.t. theta"),
+        "od": Cfg("od", B.OD_FWD, B.OD_GRAD, od_inputs, [8.0 / 3.0], ["ones(N,3)", np.float32(1.0)],
+                  ["final", "mean_z"], 50000, 0, 0, 1048576,
+                  "Lorenz RK45 ensemble (BASELINE config 4): forward + replay grad w.r.t. beta"),
     }
 
 
@@ -192,6 +206,10 @@ def oracle_step(cfg, host, n, nth):
     elif cfg.name == "q1":
         oracle.q1_fwd(host[0][:n], host[1][:n], 2.0, nthreads=nth, f64acc=False)
         oracle.q1_grad(host[0][:n], host[1][:n], 2.0, np.ones(16, np.float32), nthreads=nth)
+    elif cfg.name == "od":
+        h = [a[:n] for a in host]
+        oracle.od_fwd(*h, nthreads=nth, f64acc=False)
+        oracle.od_grad(*h, nthreads=nth)
     else:
         oracle.ph_fwd(host[0][:n], nthreads=nth, f64acc=False, libm=True)
         oracle.ph_grad(host[0][:n], nthreads=nth, libm=True)
@@ -215,7 +233,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1"])
+    ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1", "od"])
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -244,7 +262,7 @@ def main():
     host = cfg.inputs(N, rank * N, N * world)
     pi = [torch.from_numpy(h.view(np.int32) if h.dtype == np.uint32 else h).to(dev) for h in host]
     bc = [torch.tensor(v, dtype=torch.float32, device=dev) for v in cfg.bc]
-    ct = [torch.from_numpy(c).to(dev) for c in cfg.ct]
+    ct = [torch.ones((N, 3), device=dev) if isinstance(c, str) else torch.tensor(c, device=dev) for c in cfg.ct]
     fo = B.alloc_results(cfg.fwd, N, dev)
     go = B.alloc_results(cfg.grad, N, dev)
     nb = cfg.grad.tallies[0].S
@@ -301,9 +319,9 @@ def main():
     value = N * world / (tot_ms / 1e3) / 1e6
 
     # ---- e2e: the public API from pinned host inputs, H2D + both launches + result read-back timed
-    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart"}[cfg.name]
+    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz"}[cfg.name]
     F = tm.FAMILIES[fam]
-    f = tm.vmap(fam, outputs={t.name: tm.Sum(t.shape) for t in F.fwd.tallies}, in_axes=F.in_axes,
+    f = tm.vmap(fam, outputs={t.name: tm.Sum(t.dims(N)) for t in F.fwd.tallies}, in_axes=F.in_axes,
                 max_steps=cfg.max_steps)
     pinned = [p.cpu().pin_memory() for p in pi]
     wrt = tuple(i for i, ax in enumerate(F.in_axes) if ax is None)
@@ -360,6 +378,12 @@ def main():
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
     dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
+    roofline = {"bound": "issue", "kernel": dom[0], "achieved": round(achieved, 2), "peak": round(peak, 2),
+                "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
+                "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
+                "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, {cfg.tf_vjp} per step VJP; "
+                        "steps from the per-item trip counts and the replay schedule)"} if cfg.tf else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -384,12 +408,7 @@ def main():
         "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
                 "h2d_bytes_per_step": int(sum(h.nbytes for h in host)), "d2h_bytes_per_step": int(d2h[0])},
         "gpu_launches": args.steps * (2 + (1 if world > 1 else 0)),
-        "roofline": {"bound": "issue", "kernel": dom[0], "achieved": round(achieved, 2), "peak": round(peak, 2),
-                     "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": None,
-                     "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
-                     "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
-                     "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, {cfg.tf_vjp} per step "
-                             "VJP; steps from the per-item trip counts and the replay schedule)"},
+        "roofline": roofline,
         "clocks": clk,
         "kernel_resources": info,
     }

@@ -69,6 +69,8 @@ def lib():
             L.or_ph_fwd.argtypes = [i64, P, f32, f32, i32, ctypes.c_int, P, P, P, P, ctypes.c_int, ctypes.c_int]
             L.or_ph_grad.argtypes = [i64, P, f32, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P, ctypes.c_int]
             L.or_math.argtypes = [ctypes.c_int, P, P, P, i64]
+            L.or_od_fwd.argtypes = [i64, P, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
+            L.or_od_grad.argtypes = [i64, P, P, P, P, f32, P, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
             _LIB = L
     return _LIB
 
@@ -211,3 +213,40 @@ def math(fn, x, y=None):
     out = np.zeros_like(x)
     lib().or_math(MATH_FN[fn], _p(x), _p(y), _p(out), len(x))
     return out
+
+
+def od_inputs(n, seed=3):
+    """BASELINE config 4's synthetic inputs: sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2), f32"""
+    rng = np.random.default_rng(seed)
+    sigma = rng.uniform(9, 11, n).astype(np.float32)
+    rho = rng.uniform(26, 30, n).astype(np.float32)
+    y0 = (1.0 + 0.1 * rng.standard_normal((n, 3))).astype(np.float32)
+    return sigma, rho, y0, np.arange(n, dtype=np.int32)
+
+
+def od_fwd(sigma, rho, y0, item_id, beta=8.0 / 3.0, max_steps=50000, nthreads=0, f64acc=True):
+    sigma, rho = np.ascontiguousarray(sigma, np.float32), np.ascontiguousarray(rho, np.float32)
+    y0, item_id = np.ascontiguousarray(y0, np.float32), np.ascontiguousarray(item_id, np.int32)
+    n = len(sigma)
+    fin = np.zeros(3 * n, np.float32)
+    mean = np.zeros(1, np.float32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_od_fwd(n, _p(sigma), _p(rho), _p(y0), _p(item_id), np.float32(beta), max_steps, nthreads, _p(fin),
+                    _p(mean), _p(k), _p(tr), _p(st), int(f64acc))
+    return dict(final=fin.reshape(n, 3), mean=mean, k=k, trunc=tr.astype(bool), stats=st)
+
+
+def od_grad(sigma, rho, y0, item_id, beta=8.0 / 3.0, ct_final=None, ct_mean=1.0, max_steps=50000, C=16, nthreads=0):
+    sigma, rho = np.ascontiguousarray(sigma, np.float32), np.ascontiguousarray(rho, np.float32)
+    y0, item_id = np.ascontiguousarray(y0, np.float32), np.ascontiguousarray(item_id, np.int32)
+    n = len(sigma)
+    ctf = np.ones(3 * n, np.float32) if ct_final is None else np.ascontiguousarray(ct_final, np.float32).reshape(-1)
+    ctm = np.array([ct_mean], np.float32)
+    g = np.zeros(1, np.float32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_od_grad(n, _p(sigma), _p(rho), _p(y0), _p(item_id), np.float32(beta), _p(ctf), _p(ctm), max_steps, C,
+                     nthreads, _p(g), _p(tr), _p(st))
+    return dict(g=g, trunc=tr.astype(bool), stats=st)

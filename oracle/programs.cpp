@@ -378,6 +378,187 @@ static void ph_grad_run(i64 n, const u32* keys, float mu_a, float mu_s, const fl
   exact_readout(gb, 2, g, stats);
 }
 
+// ================================================================================================= OD: Lorenz RK45
+// The item of BASELINE config 4 (jax-style source in tallymap_b200/csrc/items_ode.cuh, restated here): Dormand-
+// Prince 5(4) with FSAL on the Lorenz field, RMS error norm with atol 1e-9 / rtol 1e-6, step factor
+// clip(0.9 err^-0.2, 0.2, 10) (stop_gradient'ed), t in [0, 10], h0 = 1e-3; the final state is emitted at
+// (item_id, slot) and y_z / 2^20 into a scalar.  Reverse mode restates the hand-derived VJP in the same order.
+static inline float fr(double p, double q) { return (float)(p / q); }
+struct DPT {
+  // a[i][j]: stage i+2's coefficient of k_{j+1}; b: 5th-order weights of k1..k6; e: error weights of k1..k7
+  float a[5][5], b[6], e[7];
+  DPT() {
+    const double A[5][5][2] = {{{1, 5}}, {{3, 40}, {9, 40}}, {{44, 45}, {-56, 15}, {32, 9}},
+                               {{19372, 6561}, {-25360, 2187}, {64448, 6561}, {-212, 729}},
+                               {{9017, 3168}, {-355, 33}, {46732, 5247}, {49, 176}, {-5103, 18656}}};
+    for (int i = 0; i < 5; ++i)
+      for (int j = 0; j <= i; ++j) a[i][j] = fr(A[i][j][0], A[i][j][1]);
+    const double B[6][2] = {{35, 384}, {0, 1}, {500, 1113}, {125, 192}, {-2187, 6784}, {11, 84}};
+    for (int j = 0; j < 6; ++j) b[j] = fr(B[j][0], B[j][1]);
+    const double E[7][2] = {{71, 57600}, {0, 1}, {-71, 16695}, {71, 1920}, {-17253, 339200}, {22, 525}, {-1, 40}};
+    for (int j = 0; j < 7; ++j) e[j] = fr(E[j][0], E[j][1]);
+  }
+};
+static const DPT kDP;
+
+struct OdState { i32 kc, k; float tt, h; float y[3], k1[3]; };
+
+struct OdBase {
+  const float *sigma, *rho, *y0;
+  const i32* id;
+  float beta;
+  i32 M;
+  i64 nbins;
+  static void f(float sg, float rh, float bt, const float* y, float* o) {
+    o[0] = sg * (y[1] - y[0]);
+    o[1] = y[0] * (rh - y[2]) - y[1];
+    o[2] = y[0] * y[1] - bt * y[2];
+  }
+  // stages: K[0] = k1 (given), K[1..5] = k2..k6, K[6] = k7; Z[1..5] = the stage points, Y5 = the 5th-order state
+  struct St { float K[7][3], Z[6][3], Y5[3]; };
+  static void stages(float sg, float rh, float bt, const float* y, const float* k1, float hh, St& s) {
+    for (int c = 0; c < 3; ++c) s.K[0][c] = k1[c];
+    for (int i = 1; i <= 5; ++i) {          // stage i+1: z = y + hh * (a_i0 k1 + ... )
+      for (int c = 0; c < 3; ++c) {
+        float d = kDP.a[i - 1][0] * s.K[0][c];
+        for (int j = 1; j < i; ++j) d = d + kDP.a[i - 1][j] * s.K[j][c];
+        s.Z[i][c] = y[c] + hh * d;
+      }
+      f(sg, rh, bt, s.Z[i], s.K[i]);
+    }
+    for (int c = 0; c < 3; ++c) {
+      float d = kDP.b[0] * s.K[0][c];
+      for (int j = 2; j < 6; ++j) d = d + kDP.b[j] * s.K[j][c];
+      s.Y5[c] = y[c] + hh * d;
+    }
+    f(sg, rh, bt, s.Y5, s.K[6]);
+  }
+  static bool control(const float* y, const St& s, float hh, float* fac) {
+    float q[3];
+    for (int c = 0; c < 3; ++c) {
+      float d = kDP.e[0] * s.K[0][c];
+      for (int j = 2; j < 7; ++j) d = d + kDP.e[j] * s.K[j][c];
+      const float ev = hh * d;
+      const float sc = 1e-9f + 1e-6f * std::fmax(std::fabs(y[c]), std::fabs(s.Y5[c]));
+      q[c] = ev / sc;
+    }
+    const float err = std::sqrt((q[0] * q[0] + q[1] * q[1] + q[2] * q[2]) / 3.0f);
+    const float f0 = 0.9f * tmm::powf(err, -0.2f);
+    *fac = std::fmin(std::fmax(f0, 0.2f), 10.0f);
+    return err <= 1.0f;
+  }
+  static void advance(float sg, float rh, float bt, OdState& st) {
+    const float hh = std::fmin(st.h, 10.0f - st.tt);
+    St s;
+    stages(sg, rh, bt, st.y, st.k1, hh, s);
+    float fac;
+    if (control(st.y, s, hh, &fac)) {
+      st.tt = st.tt + hh;
+      for (int c = 0; c < 3; ++c) { st.y[c] = s.Y5[c]; st.k1[c] = s.K[6][c]; }
+    }
+    st.h = hh * fac;
+    st.kc += 1;
+    st.k += 1;
+  }
+  OdState start(i64 i) const {
+    OdState s;
+    s.kc = s.k = 0;
+    s.tt = 0.0f;
+    s.h = 1e-3f;
+    for (int c = 0; c < 3; ++c) s.y[c] = y0[3 * i + c];
+    f(sigma[i], rho[i], beta, s.y, s.k1);
+    return s;
+  }
+  bool cond(const OdState& s) const { return s.kc < M && s.tt < 10.0f; }
+};
+
+template <class Acc>
+struct OdFwd : OdBase {
+  float* fin;
+  Acc* mean;
+  i32* k_out;
+  uint8_t* trunc;
+  i32* stats;
+  struct Priv { Acc m = 0; };
+  void item(i64 i, Priv& p) const {
+    OdState s = start(i);
+    while (cond(s)) advance(sigma[i], rho[i], beta, s);
+    const i32 iid = id[i];
+    for (int c = 0; c < 3; ++c) {
+      if (iid < 0 || (i64)iid * 3 + c >= nbins) stat_add(stats, 4, 1);
+      else add_out(&fin[(i64)iid * 3 + c], s.y[c]);
+    }
+    p.m += (Acc)(s.y[2] * (1.0f / 1048576.0f));
+    trunc[i] = (s.kc >= M && s.tt < 10.0f) ? 1 : 0;
+    k_out[i] = s.k;
+  }
+  void flush(Priv& p) const { if (p.m != 0) add_out(mean, p.m); }
+};
+
+struct OdGrad : OdBase {
+  const float *ctf, *ctm;
+  int C;
+  uint8_t* trunc;
+  i32* stats;
+  ExactBins* gbins;
+  float sg, rh;        // the current item's parameters
+  struct Adj { float cy[3], ck1[3], cb; };
+  struct Priv { ExactBins b{1}; };
+  OdState step(const OdState& s) const { OdState n = s; advance(sg, rh, beta, n); return n; }
+  // f's VJP at y for cotangent g: adds into cy (order as items_ode.cuh) and returns the beta term
+  float f_vjp_add(const float* y, const float* g, float* cz) const {
+    cz[0] = (-sg) * g[0] + (rh - y[2]) * g[1] + y[1] * g[2];
+    cz[1] = sg * g[0] - g[1] + y[0] * g[2];
+    cz[2] = (-(y[0] * g[1])) - beta * g[2];
+    return -(y[2] * g[2]);
+  }
+  void vjp_step(const OdState& at, Adj& a) const {
+    const float hh = std::fmin(at.h, 10.0f - at.tt);
+    St s;
+    stages(sg, rh, beta, at.y, at.k1, hh, s);
+    float fac;
+    if (!control(at.y, s, hh, &fac)) return;
+    float cz[3], ck[7][3] = {};
+    float dsum = f_vjp_add(s.Y5, a.ck1, cz);            // k7 = f(y5)
+    float cy[3], s5[3];
+    for (int c = 0; c < 3; ++c) { cy[c] = a.cy[c] + cz[c]; s5[c] = hh * cy[c]; }
+    const int bj[5] = {0, 2, 3, 4, 5};
+    for (int t = 0; t < 5; ++t)
+      for (int c = 0; c < 3; ++c) ck[bj[t]][c] = kDP.b[bj[t]] * s5[c];
+    for (int i = 5; i >= 1; --i) {                      // stages k6 .. k2
+      dsum = dsum + f_vjp_add(s.Z[i], ck[i], cz);
+      float sz[3];
+      for (int c = 0; c < 3; ++c) { cy[c] = cy[c] + cz[c]; sz[c] = hh * cz[c]; }
+      for (int j = 0; j < i; ++j)
+        for (int c = 0; c < 3; ++c) ck[j][c] = ck[j][c] + kDP.a[i - 1][j] * sz[c];
+    }
+    for (int c = 0; c < 3; ++c) { a.cy[c] = cy[c]; a.ck1[c] = ck[0][c]; }
+    a.cb = a.cb + dsum;
+  }
+  void item(i64 i, Priv& p) const {
+    OdGrad me = *this;
+    me.sg = sigma[i];
+    me.rh = rho[i];
+    const i32 iid = id[i];
+    Adj a{};
+    OdState fin;
+    checkpointed_while(me, start(i), C, a, &fin, [&](const OdState&, Adj& ad) {
+      float g[3];
+      for (int c = 0; c < 3; ++c) {
+        const bool in = iid >= 0 && (i64)iid * 3 + c < nbins;
+        g[c] = in ? ctf[(i64)iid * 3 + c] : 0.0f;
+      }
+      ad.cy[0] = g[0]; ad.cy[1] = g[1]; ad.cy[2] = g[2] + ctm[0] * (1.0f / 1048576.0f);
+      ad.ck1[0] = ad.ck1[1] = ad.ck1[2] = 0.0f;
+    });
+    trunc[i] = (fin.kc >= M && fin.tt < 10.0f) ? 1 : 0;
+    float y0v[3] = {y0[3 * i], y0[3 * i + 1], y0[3 * i + 2]}, cz[3];
+    const float db = me.f_vjp_add(y0v, a.ck1, cz);     // the pre-loop k1 = f(y0)
+    exact_emit_priv(p.b, 0, a.cb + db, stats);
+  }
+  void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
+};
+
 }  // namespace
 
 // ================================================================================================= C ABI
@@ -512,6 +693,36 @@ void or_math(int fn, const float* x, const float* y, float* out, i64 n) {
       default: out[i] = tmm::powf(x[i], y[i]); break;
     }
   }
+}
+
+int or_od_fwd(i64 n, const float* sigma, const float* rho, const float* y0, const i32* id, float beta, i32 max_steps,
+              int nthreads, float* fin, float* mean, i32* k_out, uint8_t* trunc, i32* stats, int f64acc) {
+  if (f64acc) {
+    double m = 0.0;
+    OdFwd<double> p;
+    p.sigma = sigma; p.rho = rho; p.y0 = y0; p.id = id; p.beta = beta; p.M = max_steps; p.nbins = 3 * n;
+    p.fin = fin; p.mean = &m; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+    team_run(p, n, nthreads);
+    *mean = (float)m;
+    return 0;
+  }
+  OdFwd<float> p;
+  p.sigma = sigma; p.rho = rho; p.y0 = y0; p.id = id; p.beta = beta; p.M = max_steps; p.nbins = 3 * n;
+  p.fin = fin; p.mean = mean; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+  team_run(p, n, nthreads);
+  return 0;
+}
+
+int or_od_grad(i64 n, const float* sigma, const float* rho, const float* y0, const i32* id, float beta,
+               const float* ctf, const float* ctm, i32 max_steps, int C, int nthreads, float* g, uint8_t* trunc,
+               i32* stats) {
+  ExactBins gb(1);
+  OdGrad p;
+  p.sigma = sigma; p.rho = rho; p.y0 = y0; p.id = id; p.beta = beta; p.M = max_steps; p.nbins = 3 * n;
+  p.ctf = ctf; p.ctm = ctm; p.C = C; p.trunc = trunc; p.stats = stats; p.gbins = &gb;
+  team_run(p, n, nthreads);
+  exact_readout(gb, 1, g, stats);
+  return 0;
 }
 
 }  // extern "C"

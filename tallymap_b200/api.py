@@ -54,6 +54,7 @@ FAMILIES = {
     "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100),
     "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
+    "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
 }
 
 
@@ -73,7 +74,7 @@ class Mapped:
             raise KeyError(f"tallymap_b200: item {fam.name!r} writes outputs {names}, got {sorted(outputs)}")
         for t in fam.fwd.tallies:
             o = outputs[t.name]
-            if tuple(o.shape) != tuple(t.shape) or o.dtype != t.dtype:
+            if tuple(o.shape) != tuple(t.shape) and "N" not in t.shape or o.dtype != t.dtype:
                 raise TypeError(f"tallymap_b200: output {t.name!r} is Sum({t.shape}, {t.dtype}) in this item, got "
                                 f"Sum({o.shape}, {o.dtype})")
         if tuple(in_axes) != tuple(fam.in_axes):
@@ -143,7 +144,8 @@ class Mapped:
         cts = []
         for t in self.fam.fwd.tallies:
             c = cotangents.get(t.name)
-            cts.append(torch.zeros(t.shape, dtype=t.dtype) if c is None else c)
+            n = int(pi[0].shape[0]) if pi else 0
+            cts.append(torch.zeros(t.dims(n), dtype=t.dtype) if c is None else c)
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
         ct = out[0].reshape(-1)[sel]
         trunc = out[len(prog.tallies) + 1 + prog.trunc]

@@ -33,9 +33,16 @@ class TSpec:
     exact: bool = False
     f64: bool = False      # accumulated in an f64 shadow (a scratch result), rounded once to the f32 output
 
+    def dims(self, N=None):
+        """the shape with a leading "N" (a tally indexed by item id) resolved to the launch's item count"""
+        return tuple(N if d == "N" else d for d in self.shape)
+
+    def size(self, N=None):
+        return int(np.prod(self.dims(N), dtype=np.int64)) if self.shape else 1
+
     @property
     def S(self):
-        return int(np.prod(self.shape, dtype=np.int64)) if self.shape else 1
+        return self.size()
 
 
 @dataclasses.dataclass(frozen=True)
@@ -72,13 +79,14 @@ class ItemProgram:
         scratch (replay_bytes, from replay_plan) comes last and is not zeroed."""
         out = []
         for t in self.tallies:
-            out.append((t.name, t.S * _itemsize(t.dtype), t.dtype, t.shape))
+            out.append((t.name, t.size(N) * _itemsize(t.dtype), t.dtype, t.dims(N)))
         for t in self.tallies:
+            S = t.size(N)
             if t.f64:
-                out.append((t.name + ".f64", t.S * 8, torch.float64, (t.S,)))
+                out.append((t.name + ".f64", S * 8, torch.float64, (S,)))
             if t.exact:
                 # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
-                n64 = t.S * EXACT_WORDS + (t.S + 1) // 2
+                n64 = S * EXACT_WORDS + (S + 1) // 2
                 out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
         out.append(("ctl", CTL_WORDS * 4, torch.int32, (CTL_WORDS,)))
         out.append(("stats", len(STATS) * 4, torch.int32, (len(STATS),)))
@@ -130,7 +138,19 @@ PH_GRAD = ItemProgram("ph_grad", "ph_grad", pi=(KEY,),
                       tallies=(TSpec("ct_mu", (2,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=28)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD)}
+# BASELINE config 4, the Lorenz RK45 ensemble (csrc/items_ode.cuh); "bins3": the final tally's 3N bins
+OD_PI = (Operand("sigma", (), _F32), Operand("rho", (), _F32), Operand("y0", (3,), _F32),
+         Operand("item_id", (), torch.int32))
+OD_FWD = ItemProgram("od_fwd", "od_fwd", pi=OD_PI, bc=(Operand("beta", (), _F32),), consts=("max_steps", "bins3"),
+                     tallies=(TSpec("final", ("N", 3)), TSpec("mean_z", ())),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
+OD_GRAD = ItemProgram("od_grad", "od_grad", pi=OD_PI,
+                      bc=(Operand("beta", (), _F32), Operand("ct_final", ("N", 3), _F32), Operand("ct_mean", (), _F32)),
+                      consts=("max_steps", "rev_checkpoints", "replay_threads", "bins3"),
+                      tallies=(TSpec("ct_beta", (1,), exact=True),),
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=32)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD)}
 
 
 # -------------------------------------------------------------------------------------------------- run
@@ -221,14 +241,17 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         raise ValueError("tallymap_b200: at most 2^31 - 1 items per call (tallymap/_api.py:540-542)")
     for x, o in zip(bc, p.bc):
         t = _dev(x, dev, o.dtype)
-        if tuple(t.shape) != tuple(o.shape):
-            raise TypeError(f"{p.name}: broadcast operand {o.name} has shape {tuple(t.shape)}, expected {o.shape}")
+        want = tuple(N if d == "N" else d for d in o.shape)
+        if tuple(t.shape) != want:
+            raise TypeError(f"{p.name}: broadcast operand {o.name} has shape {tuple(t.shape)}, expected {want}")
         args.append(t)
     replay_bytes = 0
+    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N}
     if p.replay_state_bytes:
-        C, threads, replay_bytes = replay_plan(p, consts[0], rev_checkpoints, dev)
-        consts = (int(consts[0]), C, threads)
-    args.append(_consts(tuple(int(c) for c in consts) or (0,), dev))
+        C, threads, replay_bytes = replay_plan(p, known["max_steps"], rev_checkpoints, dev)
+        known.update(rev_checkpoints=C, replay_threads=threads)
+    consts = tuple(known[c] for c in p.consts)
+    args.append(_consts(consts or (0,), dev))
     if order is not None:
         order = _dev(order, dev, torch.int32)
         if tuple(order.shape) != (N,):

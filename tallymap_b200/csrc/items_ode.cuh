@@ -1,0 +1,364 @@
+// Item program of the ODE-ensemble configuration: Lorenz systems integrated by adaptive
+// Dormand-Prince 5(4) (FSAL), forward and replay adjoint w.r.t. beta.  The item, as a tallymap user writes it (the
+// tableau and tolerances are Python floats, so each coefficient is a double fraction rounded once to f32):
+//
+//   def lorenz(t, sigma, rho, y0, item_id, beta):          # per item: sigma, rho, y0 (3,), item_id; broadcast: beta
+//     f = lambda y: (sigma * (y1 - y0), y0 * (rho - y2) - y1, y0 * y1 - beta * y2)
+//     def body(c):
+//       k, tt, h, y, k1, t = c
+//       hh = minimum(h, 10 - tt)
+//       k2 = f(y + hh * (a21 k1)); ...; k6 = f(y + hh * (a61 k1 + ... + a65 k5))   # sums left to right
+//       y5 = y + hh * (b1 k1 + b3 k3 + b4 k4 + b5 k5 + b6 k6);  k7 = f(y5)
+//       e = hh * (e1 k1 + e3 k3 + e4 k4 + e5 k5 + e6 k6 + e7 k7)
+//       sc = 1e-9 + 1e-6 * maximum(|y|, |y5|);  err = sqrt(((e0/sc0)^2 + (e1/sc1)^2 + (e2/sc2)^2) / 3)
+//       ok = err <= 1
+//       fac = stop_gradient(clip(0.9 * err ** -0.2, 0.2, 10.0))
+//       return k + 1, where(ok, tt + hh, tt), hh * fac, where(ok, y5, y), where(ok, k7, k1), t
+//     c = while_loop(lambda c: c[1] < 10, body, (0, 0.0, 1e-3, y0, f(y0), t))
+//     t = t.add("final", (item_id, (0, 1, 2)), y);  t = t.add("mean_z", 0, y[2] / 1048576)
+//     return t, k
+//
+// max_steps = 50,000 (retrace(cap)).  pow is tm_math.h's (bitwise equal on host and device).
+//
+// Reverse mode w.r.t. beta of <ct_final, final> + ct_mean * mean_z.  Active carries: y and k1 (tt and h are not:
+// the step-size factor is stop_gradient'ed, and err reaches nothing else: accept is a comparison).  The step VJP
+// recomputes the stages and runs them backwards (y5/k7 first, then k6 ... k2), the f VJP being
+//   ct_y0 = -sigma g0 + (rho - y2) g1 + y1 g2;  ct_y1 = sigma g0 - g1 + y0 g2;  ct_y2 = -(y0 g1) - beta g2;
+//   ct_beta = -(y2 g2)
+// each linear combination's transpose scaling by hh first (s = hh ct) and then by the coefficient; contributions
+// to the same cotangent are added in reverse order of use; beta's per-step total is summed newest stage first and
+// added to the carried f32 cotangent.  A rejected step is the identity.  Once per item: the post-loop VJP seeds
+// ct_y from ct_final[item] and ct_mean / 1048576; the pre-loop f(y0) adds its beta term; emitted into an exact bin.
+//
+// Buffers:
+//   od_fwd   sigma f32[N], rho f32[N], y0 f32[N,3], item_id i32[N], beta f32, consts i32[2], order |
+//            final f32[N*3], mean_z f32[1], ctl, stats | k i32[N], trunc u8[N]
+//   od_grad  sigma, rho, y0, item_id, beta, ct_final f32[N*3], ct_mean f32[1], consts i32[4], order |
+//            g f32[1], exact u64[6], ctl, stats | trunc u8[N], replay scratch (stored: tt, h, y, k1)
+//   (consts: max_steps, [C, replay threads,] and the final tally's bin count 3N)
+#pragma once
+#include "tm_math.h"
+#include "tm_tally.cuh"
+
+namespace tmb {
+
+struct V3 {
+  float x, y, z;
+};
+
+// Dormand-Prince 5(4): each coefficient a double fraction rounded to f32
+#define TM_F(p, q) static_cast<float>((double)(p) / (double)(q))
+struct DP {
+  static constexpr float a21 = TM_F(1, 5);
+  static constexpr float a31 = TM_F(3, 40), a32 = TM_F(9, 40);
+  static constexpr float a41 = TM_F(44, 45), a42 = TM_F(-56, 15), a43 = TM_F(32, 9);
+  static constexpr float a51 = TM_F(19372, 6561), a52 = TM_F(-25360, 2187), a53 = TM_F(64448, 6561),
+                         a54 = TM_F(-212, 729);
+  static constexpr float a61 = TM_F(9017, 3168), a62 = TM_F(-355, 33), a63 = TM_F(46732, 5247),
+                         a64 = TM_F(49, 176), a65 = TM_F(-5103, 18656);
+  static constexpr float b1 = TM_F(35, 384), b3 = TM_F(500, 1113), b4 = TM_F(125, 192), b5 = TM_F(-2187, 6784),
+                         b6 = TM_F(11, 84);
+  static constexpr float e1 = TM_F(71, 57600), e3 = TM_F(-71, 16695), e4 = TM_F(71, 1920),
+                         e5 = TM_F(-17253, 339200), e6 = TM_F(22, 525), e7 = TM_F(-1, 40);
+};
+#undef TM_F
+
+struct OdeState {
+  i32 kc, k;
+  float tt, h;
+  V3 y, k1;
+};
+
+struct OdeCommon {
+  static constexpr float kT1 = 10.0f, kAtol = 1e-9f, kRtol = 1e-6f, kInvN = 1.0f / 1048576.0f;
+  struct P {
+    float sigma, rho, beta;
+  };
+  __device__ __forceinline__ static V3 f(const P& p, const V3& y) {
+    return V3{p.sigma * (y.y - y.x), y.x * (p.rho - y.z) - y.y, y.x * y.y - p.beta * y.z};
+  }
+  __device__ __forceinline__ static V3 axpy(const V3& y, float h, const V3& d) {
+    return V3{y.x + h * d.x, y.y + h * d.y, y.z + h * d.z};
+  }
+#define TM_LIN2(c1, v1, c2, v2) V3{c1 * v1.x + c2 * v2.x, c1 * v1.y + c2 * v2.y, c1 * v1.z + c2 * v2.z}
+  struct Stages {
+    V3 k2, k3, k4, k5, k6, y5, k7, z2, z3, z4, z5, z6;
+  };
+  __device__ __forceinline__ static void stages(const P& p, const V3& y, const V3& k1, float hh, Stages& s) {
+    s.z2 = axpy(y, hh, V3{DP::a21 * k1.x, DP::a21 * k1.y, DP::a21 * k1.z});
+    s.k2 = f(p, s.z2);
+    s.z3 = axpy(y, hh, TM_LIN2(DP::a31, k1, DP::a32, s.k2));
+    s.k3 = f(p, s.z3);
+    {
+      const V3 d = V3{DP::a41 * k1.x + DP::a42 * s.k2.x + DP::a43 * s.k3.x,
+                      DP::a41 * k1.y + DP::a42 * s.k2.y + DP::a43 * s.k3.y,
+                      DP::a41 * k1.z + DP::a42 * s.k2.z + DP::a43 * s.k3.z};
+      s.z4 = axpy(y, hh, d);
+    }
+    s.k4 = f(p, s.z4);
+    {
+      const V3 d = V3{DP::a51 * k1.x + DP::a52 * s.k2.x + DP::a53 * s.k3.x + DP::a54 * s.k4.x,
+                      DP::a51 * k1.y + DP::a52 * s.k2.y + DP::a53 * s.k3.y + DP::a54 * s.k4.y,
+                      DP::a51 * k1.z + DP::a52 * s.k2.z + DP::a53 * s.k3.z + DP::a54 * s.k4.z};
+      s.z5 = axpy(y, hh, d);
+    }
+    s.k5 = f(p, s.z5);
+    {
+      const V3 d = V3{DP::a61 * k1.x + DP::a62 * s.k2.x + DP::a63 * s.k3.x + DP::a64 * s.k4.x + DP::a65 * s.k5.x,
+                      DP::a61 * k1.y + DP::a62 * s.k2.y + DP::a63 * s.k3.y + DP::a64 * s.k4.y + DP::a65 * s.k5.y,
+                      DP::a61 * k1.z + DP::a62 * s.k2.z + DP::a63 * s.k3.z + DP::a64 * s.k4.z + DP::a65 * s.k5.z};
+      s.z6 = axpy(y, hh, d);
+    }
+    s.k6 = f(p, s.z6);
+    {
+      const V3 d = V3{DP::b1 * k1.x + DP::b3 * s.k3.x + DP::b4 * s.k4.x + DP::b5 * s.k5.x + DP::b6 * s.k6.x,
+                      DP::b1 * k1.y + DP::b3 * s.k3.y + DP::b4 * s.k4.y + DP::b5 * s.k5.y + DP::b6 * s.k6.y,
+                      DP::b1 * k1.z + DP::b3 * s.k3.z + DP::b4 * s.k4.z + DP::b5 * s.k5.z + DP::b6 * s.k6.z};
+      s.y5 = axpy(y, hh, d);
+    }
+    s.k7 = f(p, s.y5);
+  }
+#undef TM_LIN2
+  // the error norm and the accept decision / factor; returns ok
+  __device__ __forceinline__ static bool control(const V3& y, const V3& k1, const Stages& s, float hh, float* fac) {
+    const float ex = hh * (DP::e1 * k1.x + DP::e3 * s.k3.x + DP::e4 * s.k4.x + DP::e5 * s.k5.x + DP::e6 * s.k6.x +
+                           DP::e7 * s.k7.x);
+    const float ey = hh * (DP::e1 * k1.y + DP::e3 * s.k3.y + DP::e4 * s.k4.y + DP::e5 * s.k5.y + DP::e6 * s.k6.y +
+                           DP::e7 * s.k7.y);
+    const float ez = hh * (DP::e1 * k1.z + DP::e3 * s.k3.z + DP::e4 * s.k4.z + DP::e5 * s.k5.z + DP::e6 * s.k6.z +
+                           DP::e7 * s.k7.z);
+    const float sx = kAtol + kRtol * fmaxf(fabsf(y.x), fabsf(s.y5.x));
+    const float sy = kAtol + kRtol * fmaxf(fabsf(y.y), fabsf(s.y5.y));
+    const float sz = kAtol + kRtol * fmaxf(fabsf(y.z), fabsf(s.y5.z));
+    const float qx = ex / sx, qy = ey / sy, qz = ez / sz;
+    const float err = sqrtf((qx * qx + qy * qy + qz * qz) / 3.0f);
+    const float f0 = 0.9f * tmm::powf(err, -0.2f);
+    *fac = fminf(fmaxf(f0, 0.2f), 10.0f);
+    return err <= 1.0f;
+  }
+  // one full step of the item's loop body (forward)
+  __device__ __forceinline__ static void advance(const P& p, OdeState& st) {
+    const float hh = fminf(st.h, kT1 - st.tt);
+    Stages s;
+    stages(p, st.y, st.k1, hh, s);
+    float fac;
+    const bool ok = control(st.y, st.k1, s, hh, &fac);
+    if (ok) {
+      st.tt = st.tt + hh;
+      st.y = s.y5;
+      st.k1 = s.k7;
+    }
+    st.h = hh * fac;
+    st.kc += 1;
+    st.k += 1;
+  }
+  // dst += coef * src
+  __device__ __forceinline__ static void acc(V3& dst, float coef, const V3& src) {
+    dst = V3{dst.x + coef * src.x, dst.y + coef * src.y, dst.z + coef * src.z};
+  }
+  // the transpose of stage k = f(z), z = y + hh * (sum a_j k_j): adds f's VJP into cy and beta's term into dsum;
+  // returns s = hh * ct_z, which each a_j then scales into ct_kj
+  __device__ __forceinline__ static V3 stage_vjp(const P& p, const V3& z, const V3& kz, float hh, float& dsum,
+                                                 V3& cy);
+  // the VJP of f at y for cotangent g: ct_y (returned) and the beta term (*db)
+  __device__ __forceinline__ static V3 f_vjp(const P& p, const V3& y, const V3& g, float* db) {
+    *db = -(y.z * g.z);
+    return V3{(-p.sigma) * g.x + (p.rho - y.z) * g.y + y.y * g.z, p.sigma * g.x - g.y + y.x * g.z,
+              (-(y.x * g.y)) - p.beta * g.z};
+  }
+};
+
+__device__ __forceinline__ V3 OdeCommon::stage_vjp(const P& p, const V3& z, const V3& kz, float hh, float& dsum,
+                                                   V3& cy) {
+  float db;
+  const V3 cz = f_vjp(p, z, kz, &db);
+  dsum = dsum + db;
+  cy = V3{cy.x + cz.x, cy.y + cz.y, cy.z + cz.z};
+  return V3{hh * cz.x, hh * cz.y, hh * cz.z};
+}
+
+struct ODFwd : OdeCommon {
+  enum { kSigma, kRho, kY0, kId, kBeta, kConsts, kOrder, kFinal, kMean, kCtl, kStats, kK, kTrunc, kNBuf };
+  enum { kConstM, kConstBins };
+  static constexpr int kSmemBytes = 16;
+  struct Ctx {
+    const float *sigma, *rho, *y0;
+    const i32* id;
+    P p;
+    i32 M;
+    i64 n_final;
+    float *fin, *mean, *sh;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+  };
+  typedef OdeState State;
+  __device__ static void setup(Ctx& c, const Params& P_, unsigned char* smem) {
+    c.sigma = static_cast<const float*>(P_.p[kSigma]);
+    c.rho = static_cast<const float*>(P_.p[kRho]);
+    c.y0 = static_cast<const float*>(P_.p[kY0]);
+    c.id = static_cast<const i32*>(P_.p[kId]);
+    c.p.beta = __ldg(static_cast<const float*>(P_.p[kBeta]));
+    c.M = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstM);
+    c.n_final = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstBins);
+    c.fin = static_cast<float*>(P_.p[kFinal]);
+    c.mean = static_cast<float*>(P_.p[kMean]);
+    c.sh = reinterpret_cast<float*>(smem);
+    c.stats = static_cast<i32*>(P_.p[kStats]);
+    c.kout = static_cast<i32*>(P_.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P_.p[kTrunc]);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static State start(Ctx& c, i64 item) {
+    c.p.sigma = __ldg(&c.sigma[item]);
+    c.p.rho = __ldg(&c.rho[item]);
+    const V3 y{__ldg(&c.y0[3 * item]), __ldg(&c.y0[3 * item + 1]), __ldg(&c.y0[3 * item + 2])};
+    return State{0, 0, 0.0f, 1e-3f, y, f(c.p, y)};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.tt < kT1; }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s) { advance(c.p, s); }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item) {
+    // final: Sum((N, 3)) at (item_id, slot), each bin written by one item (a tuple index: out of range -> dropped)
+    const i32 iid = __ldg(&c.id[item]);
+    const float v[3] = {s.y.x, s.y.y, s.y.z};
+    for (int j = 0; j < 3; ++j) {
+      if (iid < 0 || (i64)iid * 3 + j >= c.n_final) atomicAdd(&c.stats[kStDroppedEmits], 1);
+      else fatom(&c.fin[(i64)iid * 3 + j], v[j]);
+    }
+    fatom(c.sh, s.y.z * kInvN);            // mean_z: privatised in shared memory
+    c.kout[item] = s.k;
+    c.trunc[item] = (s.kc >= c.M && s.tt < kT1) ? 1 : 0;
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int) {
+    if (tid == 0) {
+      const float v = *reinterpret_cast<const float*>(smem);
+      if (v != 0.0f) fatom(c.mean, v);
+    }
+  }
+  __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
+struct ODGrad : OdeCommon {
+  enum { kSigma, kRho, kY0, kId, kBeta, kCtFinal, kCtMean, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc,
+         kReplay, kNBuf };
+  enum { kConstM, kConstC, kConstThreads, kConstBins };
+  static constexpr int kSmemBytes = ExactBins<1>::kSmemBytes;
+  struct Ctx {
+    const float *sigma, *rho, *y0;
+    const i32* id;
+    P p;
+    i32 M, iid;
+    i64 n_final;
+    const float *ctf, *ctm;
+    u64* gw;
+    float* g;
+    i32* stats;
+    uint8_t* trunc;
+    V3 y_init;
+    mutable ExactPriv<1> pv;
+  };
+  typedef OdeState State;
+  struct Adj {
+    V3 cy, ck1;
+    float cb;
+  };
+  struct Stored {
+    float tt, h;
+    V3 y, k1;
+  };
+  __device__ static void setup(Ctx& c, const Params& P_, unsigned char*) {
+    c.sigma = static_cast<const float*>(P_.p[kSigma]);
+    c.rho = static_cast<const float*>(P_.p[kRho]);
+    c.y0 = static_cast<const float*>(P_.p[kY0]);
+    c.id = static_cast<const i32*>(P_.p[kId]);
+    c.p.beta = __ldg(static_cast<const float*>(P_.p[kBeta]));
+    c.M = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstM);
+    c.n_final = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstBins);
+    c.ctf = static_cast<const float*>(P_.p[kCtFinal]);
+    c.ctm = static_cast<const float*>(P_.p[kCtMean]);
+    c.gw = static_cast<u64*>(P_.p[kExact]);
+    c.g = static_cast<float*>(P_.p[kG]);
+    c.stats = static_cast<i32*>(P_.p[kStats]);
+    c.trunc = static_cast<uint8_t*>(P_.p[kTrunc]);
+    c.pv.zero();
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static State start(Ctx& c, i64 item) {
+    c.p.sigma = __ldg(&c.sigma[item]);
+    c.p.rho = __ldg(&c.rho[item]);
+    c.y_init = V3{__ldg(&c.y0[3 * item]), __ldg(&c.y0[3 * item + 1]), __ldg(&c.y0[3 * item + 2])};
+    c.iid = __ldg(&c.id[item]);
+    return State{0, 0, 0.0f, 1e-3f, c.y_init, f(c.p, c.y_init)};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.tt < kT1; }
+  __device__ __forceinline__ static Stored store(const State& s) { return Stored{s.tt, s.h, s.y, s.k1}; }
+  __device__ __forceinline__ static State restore(const Ctx&, const Stored& v, i64 step) {
+    return State{(i32)step, (i32)step, v.tt, v.h, v.y, v.k1};
+  }
+  __device__ static void adj_start(const Ctx&, Adj& a) {
+    a.cy = V3{0.0f, 0.0f, 0.0f};
+    a.ck1 = V3{0.0f, 0.0f, 0.0f};
+    a.cb = 0.0f;
+  }
+  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) { advance(c.p, s); }
+  __device__ static void vjp(const Ctx& c, const State& at, Adj& a) {
+    const float hh = fminf(at.h, kT1 - at.tt);
+    Stages s;
+    stages(c.p, at.y, at.k1, hh, s);
+    float fac;
+    if (!control(at.y, at.k1, s, hh, &fac)) return;   // rejected: the identity
+    float db, dsum;
+    // k7 = f(y5); y' = y5
+    V3 cy5 = f_vjp(c.p, s.y5, a.ck1, &db);
+    dsum = db;
+    cy5 = V3{a.cy.x + cy5.x, a.cy.y + cy5.y, a.cy.z + cy5.z};
+    // y5 = y + hh * (b1 k1 + b3 k3 + b4 k4 + b5 k5 + b6 k6)
+    const V3 s5{hh * cy5.x, hh * cy5.y, hh * cy5.z};
+    V3 cy = cy5;
+    V3 ck1{DP::b1 * s5.x, DP::b1 * s5.y, DP::b1 * s5.z};
+    V3 ck2{0.0f, 0.0f, 0.0f};
+    V3 ck3{DP::b3 * s5.x, DP::b3 * s5.y, DP::b3 * s5.z};
+    V3 ck4{DP::b4 * s5.x, DP::b4 * s5.y, DP::b4 * s5.z};
+    V3 ck5{DP::b5 * s5.x, DP::b5 * s5.y, DP::b5 * s5.z};
+    V3 ck6{DP::b6 * s5.x, DP::b6 * s5.y, DP::b6 * s5.z};
+    V3 sz = stage_vjp(c.p, s.z6, ck6, hh, dsum, cy);
+    acc(ck1, DP::a61, sz); acc(ck2, DP::a62, sz); acc(ck3, DP::a63, sz); acc(ck4, DP::a64, sz); acc(ck5, DP::a65, sz);
+    sz = stage_vjp(c.p, s.z5, ck5, hh, dsum, cy);
+    acc(ck1, DP::a51, sz); acc(ck2, DP::a52, sz); acc(ck3, DP::a53, sz); acc(ck4, DP::a54, sz);
+    sz = stage_vjp(c.p, s.z4, ck4, hh, dsum, cy);
+    acc(ck1, DP::a41, sz); acc(ck2, DP::a42, sz); acc(ck3, DP::a43, sz);
+    sz = stage_vjp(c.p, s.z3, ck3, hh, dsum, cy);
+    acc(ck1, DP::a31, sz); acc(ck2, DP::a32, sz);
+    sz = stage_vjp(c.p, s.z2, ck2, hh, dsum, cy);
+    acc(ck1, DP::a21, sz);
+    a.cy = cy;
+    a.ck1 = ck1;
+    a.cb = a.cb + dsum;
+  }
+  // the post-loop emits' transpose: the final state's cotangent is ct_final at the item's bins (0 for a dropped
+  // emit) plus ct_mean / N on z
+  __device__ static void post_vjp(const Ctx& c, const State&, Adj& a) {
+    float g[3];
+    for (int j = 0; j < 3; ++j) {
+      const bool in = c.iid >= 0 && (i64)c.iid * 3 + j < c.n_final;
+      g[j] = in ? __ldg(&c.ctf[(i64)c.iid * 3 + j]) : 0.0f;
+    }
+    a.cy = V3{g[0], g[1], g[2] + __ldg(c.ctm) * kInvN};
+  }
+  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {
+    c.trunc[item] = (fin.kc >= c.M && fin.tt < kT1) ? 1 : 0;
+    // the pre-loop k1 = f(y0): its beta term (y0 is an input, not differentiated)
+    float db;
+    f_vjp(c.p, c.y_init, a.ck1, &db);
+    const float g = a.cb + db;
+    if (c.pv.emit(0, g)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+  }
+  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
+    ExactBins<1>::flush(c.pv, smem, c.gw, c.stats, tid);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
+    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
+  }
+};
+
+}  // namespace tmb

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/tallymap_b200.h"
+#include "items_ode.cuh"
 #include "items_photon.cuh"
 #include "items_walks.cuh"
 #include "tm_aux.cuh"
@@ -93,6 +94,8 @@ void init_registry() {
   add_replay<tmb::RWGrad, 4>("rw_grad");
   add_forward<tmb::PHFwd>("ph_fwd");
   add_replay<tmb::PHGrad, 1>("ph_grad");
+  add_forward<tmb::ODFwd>("od_fwd");
+  add_replay<tmb::ODGrad, 1>("od_grad");
 }
 
 Kernel* find(int64_t id) {
