@@ -70,6 +70,7 @@ def lib():
             L.or_ph_grad.argtypes = [i64, P, f32, f32, P, i32, ctypes.c_int, ctypes.c_int, P, P, P, ctypes.c_int]
             L.or_math.argtypes = [ctypes.c_int, P, P, P, i64]
             L.or_od_fwd.argtypes = [i64, P, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
+            L.or_sh_fwd.argtypes = [i64, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
             L.or_od_grad.argtypes = [i64, P, P, P, P, f32, P, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
             _LIB = L
     return _LIB
@@ -250,3 +251,28 @@ def od_grad(sigma, rho, y0, item_id, beta=8.0 / 3.0, ct_final=None, ct_mean=1.0,
     lib().or_od_grad(n, _p(sigma), _p(rho), _p(y0), _p(item_id), np.float32(beta), _p(ctf), _p(ctm), max_steps, C,
                      nthreads, _p(g), _p(tr), _p(st))
     return dict(g=g, trunc=tr.astype(bool), stats=st)
+
+
+def sh_inputs(n, seed=5):
+    """BASELINE config 5's primaries: E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
+    import sys
+    import os
+    sys.path.insert(0, os.path.dirname(HERE))
+    from tallymap_b200 import prng
+    rng = np.random.default_rng(seed)
+    E0 = np.exp(rng.uniform(0.0, np.log(1000.0), n)).astype(np.float32)
+    return E0, np.zeros(n, np.float32), prng.split(prng.PRNGKey(5), n)
+
+
+def sh_fwd(E0, d0, keys, X0=1.0, max_steps=100000, nthreads=0, f64acc=True):
+    E0, d0 = np.ascontiguousarray(E0, np.float32), np.ascontiguousarray(d0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    n = len(E0)
+    dep = np.zeros(512, np.float32)
+    count = np.zeros(1, np.int32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_sh_fwd(n, _p(E0), _p(d0), _p(keys), X0, max_steps, nthreads, _p(dep), _p(count), _p(k), _p(tr), _p(st),
+                    int(f64acc))
+    return dict(dep=dep, count=count, k=k, trunc=tr.astype(bool), stats=st)

@@ -559,6 +559,79 @@ struct OdGrad : OdBase {
   void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
 };
 
+// ================================================================================================= SH: shower
+// The item of BASELINE config 5 (jax-style source in tallymap_b200/csrc/items_shower.cuh, restated here).  The
+// reference runs spawned children through a shared ticket ring on its OpenMP team (kernel.py:778-811, 1007-1044);
+// every child is an independent item, so when the ring drops nothing the tallies are the same sums whatever order
+// the children run in.  The oracle therefore runs each root's whole tree depth-first on one thread (a private stack
+// of pending children), which is that schedule with an unbounded ring: the spawned count is every child.
+struct ShChild { float E, depth; Key key; };
+
+template <class Acc>
+struct ShFwd {
+  const float *E0, *d0;
+  const u32* keys;
+  float X0;
+  i32 M;
+  Acc* dep;            // [512]
+  i32* count;
+  i32* k_out;
+  uint8_t* trunc;
+  i32* stats;
+  struct Priv { Acc h[512] = {}; i64 n = 0, spawned = 0, ctrunc = 0; std::vector<ShChild> stack; };
+  // run one particle; pushes its children; returns (k, truncated)
+  void particle(ShChild p, Priv& pv, i32* k_ret, bool* tr_ret) const {
+    i32 kc = 0, k = 0;
+    bool alive = true;
+    float E = p.E, depth = p.depth;
+    while (kc < M && alive) {
+      const Key kk = fold_in(p.key, (u32)k);
+      const float u0 = uniform_f32(kk, 0u, 0.0f, 1.0f), u1 = uniform_f32(kk, 1u, 0.0f, 1.0f);
+      const float u2 = uniform_f32(kk, 2u, 0.0f, 1.0f);
+      depth = depth + X0 * (-tmm::logf(1.0f - u0));
+      const bool low = E < 0.5f;
+      if (low) {
+        const i32 b = f2i_rz(depth * 8.0f);
+        if ((u32)b >= 512u) stat_add(stats, 4, 1); else pv.h[b] += (Acc)E;
+      }
+      const bool split = !low && u1 < 0.7f;
+      if (split) {
+        const float z = 0.1f + 0.8f * u2;
+        pv.stack.push_back(ShChild{E * (1.0f - z), depth, fold_in(kk, 1u)});   // popped second
+        pv.stack.push_back(ShChild{E * z, depth, fold_in(kk, 0u)});
+        pv.spawned += 2;
+      }
+      alive = !low && !split;
+      kc += 1;
+      k += 1;
+    }
+    pv.n += 1;
+    *k_ret = k;
+    *tr_ret = kc >= M && alive;
+  }
+  void item(i64 i, Priv& pv) const {
+    i32 k;
+    bool tr;
+    particle(ShChild{E0[i], d0[i], Key{keys[2 * i], keys[2 * i + 1]}}, pv, &k, &tr);
+    k_out[i] = k;
+    trunc[i] = tr ? 1 : 0;
+    while (!pv.stack.empty()) {
+      const ShChild c = pv.stack.back();
+      pv.stack.pop_back();
+      i32 kk;
+      bool t2;
+      particle(c, pv, &kk, &t2);
+      if (t2) pv.ctrunc += 1;
+    }
+  }
+  void flush(Priv& pv) const {
+    for (int b = 0; b < 512; ++b) if (pv.h[b] != 0) add_out(&dep[b], pv.h[b]);
+    stat_add(count, 0, (i32)pv.n);
+    stat_add(stats, 0, (i32)pv.spawned);
+    stat_add(stats, 2, (i32)pv.ctrunc);
+  }
+};
+
 }  // namespace
 
 // ================================================================================================= C ABI
@@ -722,6 +795,24 @@ int or_od_grad(i64 n, const float* sigma, const float* rho, const float* y0, con
   p.ctf = ctf; p.ctm = ctm; p.C = C; p.trunc = trunc; p.stats = stats; p.gbins = &gb;
   team_run(p, n, nthreads);
   exact_readout(gb, 1, g, stats);
+  return 0;
+}
+
+int or_sh_fwd(i64 n, const float* E0, const float* d0, const u32* keys, float X0, i32 max_steps, int nthreads,
+              float* dep, i32* count, i32* k_out, uint8_t* trunc, i32* stats, int f64acc) {
+  if (f64acc) {
+    std::vector<double> d(512, 0.0);
+    ShFwd<double> p;
+    p.E0 = E0; p.d0 = d0; p.keys = keys; p.X0 = X0; p.M = max_steps;
+    p.dep = d.data(); p.count = count; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+    team_run(p, n, nthreads);
+    for (int b = 0; b < 512; ++b) dep[b] = (float)d[b];
+    return 0;
+  }
+  ShFwd<float> p;
+  p.E0 = E0; p.d0 = d0; p.keys = keys; p.X0 = X0; p.M = max_steps;
+  p.dep = dep; p.count = count; p.k_out = k_out; p.trunc = trunc; p.stats = stats;
+  team_run(p, n, nthreads);
   return 0;
 }
 

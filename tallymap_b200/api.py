@@ -55,6 +55,7 @@ FAMILIES = {
     "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
+    "shower": Family("shower", B.SH_FWD, {}, (0, 0, 0, None), 100000),
 }
 
 

@@ -21,6 +21,8 @@ from . import _lib
 STATS = ("spawned", "children_dropped", "children_truncated", "fixed_point_overflow", "dropped_emits")
 CTL_WORDS = 8
 EXACT_WORDS = 5
+QCTL_WORDS = 5 * 32         # the spawn ring's control words, one 128-byte line each
+QUEUE_DEFAULT = 1 << 22     # ring slots of a spawning program (64 MiB of leaves for the shower)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -69,14 +71,16 @@ class ItemProgram:
     trunc: int = None
     spawns: bool = False
     replay_state_bytes: int = 0     # an adjoint: bytes of one stored loop state in its replay scratch
+    queue_leaf_bytes: int = 0       # a spawning program: bytes of one child's leaves in the ring
 
     @property
     def n_args(self):
         return len(self.pi) + len(self.bc) + 2     # + hoisted constants + the optional claim order
 
-    def result_layout(self, N, replay_bytes=0):
+    def result_layout(self, N, replay_bytes=0, queue=0):
         """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero.  An adjoint's replay
-        scratch (replay_bytes, from replay_plan) comes last and is not zeroed."""
+        scratch (replay_bytes, from replay_plan) comes last and is not zeroed; a spawning program's ring of `queue`
+        slots: its sequence and control words are zeroed (an empty ring), its leaves come last, not zeroed."""
         out = []
         for t in self.tallies:
             out.append((t.name, t.size(N) * _itemsize(t.dtype), t.dtype, t.dims(N)))
@@ -88,6 +92,9 @@ class ItemProgram:
                 # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
                 n64 = S * EXACT_WORDS + (S + 1) // 2
                 out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
+        if self.queue_leaf_bytes:
+            out.append(("queue.seq", max(queue, 1) * 4, torch.int32, (max(queue, 1),)))
+            out.append(("queue.ctl", QCTL_WORDS * 4, torch.int32, (QCTL_WORDS,)))
         out.append(("ctl", CTL_WORDS * 4, torch.int32, (CTL_WORDS,)))
         out.append(("stats", len(STATS) * 4, torch.int32, (len(STATS),)))
         n_zero = len(out)
@@ -97,6 +104,9 @@ class ItemProgram:
         if self.replay_state_bytes:
             n = max(1, (replay_bytes + 15) // 16)
             out.append(("replay", n * 16, torch.int32, (n * 4,)))
+        if self.queue_leaf_bytes:
+            n = max(queue, 1) * self.queue_leaf_bytes // 4
+            out.append(("queue.ring", n * 4, torch.int32, (n,)))
         return out, n_zero
 
 
@@ -150,7 +160,14 @@ OD_GRAD = ItemProgram("od_grad", "od_grad", pi=OD_PI,
                       tallies=(TSpec("ct_beta", (1,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=32)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD)}
+# BASELINE config 5, the branching shower (csrc/items_shower.cuh): a spawning program with a ring of Q slots
+SH_FWD = ItemProgram("sh_fwd", "sh_fwd", pi=(Operand("E", (), _F32), Operand("depth", (), _F32), KEY),
+                     bc=(Operand("X0", (), _F32),), consts=("max_steps", "queue"),
+                     tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32)),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1, spawns=True,
+                     queue_leaf_bytes=16)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD, SH_FWD)}
 
 
 # -------------------------------------------------------------------------------------------------- run
@@ -215,7 +232,8 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
     return C, threads, threads * per(C)
 
 
-def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, order=None, **_):
+def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, order=None,
+        queue=None, **_):
     """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
     and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
     as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
@@ -246,7 +264,8 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
             raise TypeError(f"{p.name}: broadcast operand {o.name} has shape {tuple(t.shape)}, expected {want}")
         args.append(t)
     replay_bytes = 0
-    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N}
+    Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
+    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q}
     if p.replay_state_bytes:
         C, threads, replay_bytes = replay_plan(p, known["max_steps"], rev_checkpoints, dev)
         known.update(rev_checkpoints=C, replay_threads=threads)
@@ -257,8 +276,8 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         if tuple(order.shape) != (N,):
             raise TypeError(f"{p.name}: order has shape {tuple(order.shape)}, expected {(N,)}")
     args.append(order)
-    layout, n_zero = p.result_layout(N, replay_bytes)
-    res = out if out is not None else alloc_results(p, N, dev, replay_bytes)
+    layout, n_zero = p.result_layout(N, replay_bytes, Q)
+    res = out if out is not None else alloc_results(p, N, dev, replay_bytes, Q)
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
     kid, nbuf = _lib.kernel_id(p.kernel)
@@ -271,7 +290,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     names = [n for n, _, _, _ in layout]
     tallies = [res[names.index(t.name)] for t in p.tallies]
     ys = res[n_zero:n_zero + len(p.ys)]
-    run.last = dict(ctl=res[names.index("ctl")], args=args, consts=consts)
+    run.last = dict(ctl=res[names.index("ctl")], args=args, consts=consts, results=dict(zip(names, res)))
     return tallies + [res[names.index("stats")]] + list(ys)
 
 
@@ -288,12 +307,14 @@ def _consts(vals, dev):
     return t
 
 
-def alloc_results(p, N, device=None, replay_bytes=None):
-    """result buffers for N items (an adjoint's replay scratch as planned on `device` unless given)."""
+def alloc_results(p, N, device=None, replay_bytes=None, queue=None):
+    """result buffers for N items (an adjoint's replay scratch as planned on `device` unless given; a spawning
+    program's ring of `queue` slots)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     if replay_bytes is None and p.replay_state_bytes:
         replay_bytes = replay_plan(p, 2 ** 31 - 1, None, device)[2]
-    layout, _ = p.result_layout(N, replay_bytes or 0)
+    Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
+    layout, _ = p.result_layout(N, replay_bytes or 0, Q)
     return [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout]
 
 

@@ -18,6 +18,7 @@
 #include "../../include/tallymap_b200.h"
 #include "items_ode.cuh"
 #include "items_photon.cuh"
+#include "items_shower.cuh"
 #include "items_walks.cuh"
 #include "tm_aux.cuh"
 
@@ -71,6 +72,17 @@ void add_forward(const char* name) {
   g_names->push_back(name);
 }
 
+template <class I>
+void add_spawn(const char* name) {
+  Kernel k;
+  k.name = name;
+  k.fn = reinterpret_cast<const void*>(&tmb::spawn_kernel<I>);
+  k.nbuf = I::kNBuf;
+  k.smem = I::kSmemBytes;
+  (*g_reg)[name_id(name)] = k;
+  g_names->push_back(name);
+}
+
 template <class I, int V>
 void add_replay(const char* name) {
   Kernel k;
@@ -96,6 +108,7 @@ void init_registry() {
   add_replay<tmb::PHGrad, 1>("ph_grad");
   add_forward<tmb::ODFwd>("od_fwd");
   add_replay<tmb::ODGrad, 1>("od_grad");
+  add_spawn<tmb::SHFwd>("sh_fwd");
 }
 
 Kernel* find(int64_t id) {
