@@ -43,15 +43,25 @@ def all_reduce_sums(tensors):
     return tensors
 
 
+def gather_words(words):
+    """every rank's exact scratch words, stacked [world, n] (all_gather; 40 bytes per bin per rank)."""
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    if world == 1:
+        return words.reshape(1, -1)
+    if dist.get_backend() == "nccl":
+        gathered = torch.empty((world, words.numel()), dtype=words.dtype, device=words.device)
+        dist.all_gather_into_tensor(gathered, words.reshape(-1))
+        return gathered
+    parts = [torch.empty_like(words.reshape(-1)) for _ in range(world)]
+    dist.all_gather(parts, words.reshape(-1).contiguous())
+    return torch.stack(parts)
+
+
 def combine_exact(words, n_bins, out, stats):
     """the cross-rank total of an exact tally: all_gather every rank's scratch words (int64, the layout of
     tm_exact_combine), then combine and read out on this device into `out` (f32[n_bins])."""
-    world = dist.get_world_size() if dist.is_initialized() else 1
-    if world == 1:
-        gathered = words.reshape(1, -1)
-    else:
-        gathered = torch.empty((world, words.numel()), dtype=words.dtype, device=words.device)
-        dist.all_gather_into_tensor(gathered, words.reshape(-1))
+    gathered = gather_words(words)
+    world = gathered.shape[0]
     st = torch.cuda.current_stream(words.device).cuda_stream
     _lib.check(_lib.lib().tm_exact_combine(ctypes.c_void_p(st), ctypes.c_void_p(gathered.data_ptr()), world, n_bins,
                                            ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stats.data_ptr())))

@@ -1,0 +1,80 @@
+"""Items sharded over 2 GPUs (one NCCL rank per GPU) against one GPU, as the reference's sharding test
+(tests/sharding.py:112-122): per-item results of each shard bitwise, the exact gradient bitwise (its words are
+all_gathered and combined with carries), float tallies within 1e-4 (the reference's tolerance for a sharded run).
+Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def rw_inputs(n):
+    from tallymap_b200 import prng
+    kx, ks = prng.split(prng.PRNGKey(1), 2)
+    return prng.uniform(kx, n), prng.split(ks, n)
+
+
+def _rank(rank, world, port, n, q):
+    import torch.distributed as dist
+    from tallymap_b200 import backend as B
+    from tallymap_b200 import parallel
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        x, k = rw_inputs(n)
+        s0, c = parallel.shard(n, rank, world)
+        f = B.run(B.RW_FWD, [x[s0:s0 + c], k[s0:s0 + c]], [np.float32(1.0)], consts=(20000,))
+        parallel.all_reduce_sums(f[:3])
+        g = B.run(B.RW_GRAD, [x[s0:s0 + c], k[s0:s0 + c]],
+                  [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)], consts=(20000,))
+        words = B.run.last["results"]["ct_drift.exact"]
+        gall = torch.zeros(1, device=dev)
+        st = torch.zeros(5, dtype=torch.int32, device=dev)
+        parallel.combine_exact(words, 1, gall, st)
+        torch.cuda.synchronize()
+        q.put((rank, f[0].cpu().numpy(), f[1].cpu().numpy(), f[3].cpu().numpy(), gall.cpu().numpy()))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_sharding_matches_one(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from tallymap_b200 import backend as B
+    n = 200003
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, n, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    x, k = rw_inputs(n)
+    one = B.run(B.RW_FWD, [x, k], [np.float32(1.0)], consts=(20000,))
+    g1 = B.run(B.RW_GRAD, [x, k], [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)],
+               consts=(20000,))
+    hist1, side1, k1 = one[0].cpu().numpy(), one[1].cpu().numpy(), one[3].cpu().numpy()
+    assert np.array_equal(np.concatenate([res[0][3], res[1][3]]), k1)
+    for r in res:
+        assert np.abs(r[1].astype(np.float64) - hist1).max() <= 1e-4 * np.abs(hist1).max()
+        assert np.array_equal(r[2], side1)
+        assert r[4].view(np.uint32)[0] == g1[0].cpu().numpy().view(np.uint32)[0]
