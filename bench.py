@@ -38,6 +38,13 @@ N_ITEMS = 4194304
 MAX_STEPS = 20000
 TF_OPS = 79          # INT32 ops per threefry2x32 (2 XOR + 2 ADD + 20 x (ADD, ROTL, XOR) + 5 x 3 ADD)
 METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per item of one launch, from the ncu captures summarised
+# under profiles/ (kernel -> (bytes per item, items in the capture)); the bench scales them to its own launch
+TRAFFIC = {
+    "rw_grad": ((5.241173e9 + 6.034955e9) / 1048576, 1048576),
+    "rw_fwd": ((52.543232e6 + 4.872960e6) / 4194304, 4194304),
+    "ph_fwd": ((10.557440e6 + 0.0) / 1048576, 1048576),
+}
 
 
 def rw_inputs(n, start=0, total=None):
@@ -378,8 +385,12 @@ def main():
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
     dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
+    tr = TRAFFIC.get(dom[0])
+    traffic = None if tr is None else int(round(tr[0] * N))
     roofline = {"bound": "issue", "kernel": dom[0], "achieved": round(achieved, 2), "peak": round(peak, 2),
-                "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "unit": "Gthreefry/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "traffic_source": None if tr is None else
+                f"ncu dram bytes read+write of one launch at N={tr[1]}, scaled by items to N={N}",
                 "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
                 "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
                 "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, {cfg.tf_vjp} per step VJP; "
