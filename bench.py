@@ -71,6 +71,15 @@ def od_inputs(n, start=0, total=None):
     return sigma.copy(), rho.copy(), y0.copy(), np.arange(start, start + n, dtype=np.int32)
 
 
+def sh_inputs(n, start=0, total=None):
+    """E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
+    from tallymap_b200 import prng
+    total = total or start + n
+    rng = np.random.default_rng(5)
+    E0 = np.exp(rng.uniform(0.0, np.log(1000.0), total)).astype(np.float32)[start:start + n]
+    return E0.copy(), np.zeros(n, np.float32), prng.split(prng.PRNGKey(5), n, start=start)
+
+
 def ph_inputs(n, start=0, total=None):
     from tallymap_b200 import prng
     return (prng.split(prng.PRNGKey(2), n, start=start),)
@@ -99,6 +108,11 @@ def configs(B):
         "od": Cfg("od", B.OD_FWD, B.OD_GRAD, od_inputs, [8.0 / 3.0], ["ones(N,3)", np.float32(1.0)],
                   ["final", "mean_z"], 50000, 0, 0, 1048576,
                   "Lorenz RK45 ensemble (BASELINE config 4): forward + replay grad w.r.t. beta"),
+        # the gradient is the tree adjoint: the recording forward, the generation lists, one adjoint launch per
+        # generation and one over the roots (backend.tree_grad)
+        "sh": Cfg("sh", B.SH_FWD, B.SH_GRAD, sh_inputs, [1.0], [np.ones(512, np.float32)], ["dep", "count"], 100000,
+                  0, 0, 1048576,
+                  "branching shower (BASELINE config 5): forward + tree-adjoint grad w.r.t. X0 (items = roots)"),
     }
 
 
@@ -217,6 +231,10 @@ def oracle_step(cfg, host, n, nth):
         h = [a[:n] for a in host]
         oracle.od_fwd(*h, nthreads=nth, f64acc=False)
         oracle.od_grad(*h, nthreads=nth)
+    elif cfg.name == "sh":
+        h = [a[:n] for a in host]
+        oracle.sh_fwd(*h, nthreads=nth, f64acc=False)
+        oracle.sh_grad(*h, nthreads=nth)
     else:
         oracle.ph_fwd(host[0][:n], nthreads=nth, f64acc=False, libm=True)
         oracle.ph_grad(host[0][:n], nthreads=nth, libm=True)
@@ -240,7 +258,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1", "od"])
+    ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1", "od", "sh"])
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -270,14 +288,16 @@ def main():
     pi = [torch.from_numpy(h.view(np.int32) if h.dtype == np.uint32 else h).to(dev) for h in host]
     bc = [torch.tensor(v, dtype=torch.float32, device=dev) for v in cfg.bc]
     ct = [torch.ones((N, 3), device=dev) if isinstance(c, str) else torch.tensor(c, device=dev) for c in cfg.ct]
+    tree = cfg.name == "sh"
     fo = B.alloc_results(cfg.fwd, N, dev)
-    go = B.alloc_results(cfg.grad, N, dev)
+    go = None if tree else B.alloc_results(cfg.grad, N, dev)
     nb = cfg.grad.tallies[0].S
     g_all = torch.zeros(nb, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    gnames = [n for n, _, _, _ in cfg.grad.result_layout(N)[0]]
+    gnames = None if tree else [n for n, _, _, _ in cfg.grad.result_layout(N)[0]]
     ntal = len(cfg.fwd.tallies)
+    tree_info = {}
 
     def fwd():
         out = B.run(cfg.fwd, pi, bc, consts=(cfg.max_steps,), out=fo)
@@ -286,6 +306,12 @@ def main():
         return out
 
     def grad():
+        if tree:
+            r = B.tree_grad(pi, bc[0], ct[0], max_steps=cfg.max_steps)
+            tree_info.update(r["info"])
+            if world > 1:
+                parallel.combine_exact(r["words"], nb, g_all, r["stats"])
+            return r
         # the replay claims items longest first by the forward's trip counts (as value_and_grad does)
         order = longest_first(fo[-2])
         out = B.run(cfg.grad, pi, bc + ct, consts=(cfg.max_steps,), out=go, order=order)
@@ -326,9 +352,9 @@ def main():
     value = N * world / (tot_ms / 1e3) / 1e6
 
     # ---- e2e: the public API from pinned host inputs, H2D + both launches + result read-back timed
-    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz"}[cfg.name]
+    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz", "sh": "shower"}[cfg.name]
     F = tm.FAMILIES[fam]
-    f = tm.vmap(fam, outputs={t.name: tm.Sum(t.dims(N)) for t in F.fwd.tallies}, in_axes=F.in_axes,
+    f = tm.vmap(fam, outputs={t.name: tm.Sum(t.dims(N), t.dtype) for t in F.fwd.tallies}, in_axes=F.in_axes,
                 max_steps=cfg.max_steps)
     pinned = [p.cpu().pin_memory() for p in pi]
     wrt = tuple(i for i, ax in enumerate(F.in_axes) if ax is None)
@@ -364,7 +390,8 @@ def main():
     e2e_val = N * world / (float(te.item()) / 1e3) / 1e6
 
     # ---- roofline of the dominant kernel: threefry2x32 evaluations per second against the probe's
-    kk = fo[-2].to("cpu").numpy()
+    fnames = [n for n, _, _, _ in cfg.fwd.result_layout(N, 0, B.QUEUE_DEFAULT if tree else 0)[0]]
+    kk = fo[fnames.index("k")].to("cpu").numpy()
     steps_total = int(kk.astype(np.int64).sum())
     tf_fwd = cfg.tf * steps_total
     C_used = B.replay_plan(cfg.grad, cfg.max_steps, None, dev)[0]
@@ -416,9 +443,13 @@ def main():
         "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),
         "grad_mitems_s": round(N * world / (g_ms / 1e3) / 1e6, 3),
         "mean_trip_count": round(steps_total / N, 2),
+        **({"particles_per_gpu": int(fo[fnames.index("count")][0].item()),
+            "particles_mnodes_s": round(int(fo[fnames.index("count")][0].item()) * world / (tot_ms / 1e3) / 1e6, 3),
+            "tree_generations": tree_info.get("generations"), "tree_adjoint_launches": tree_info.get("launches")}
+           if tree else {}),
         "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
                 "h2d_bytes_per_step": int(sum(h.nbytes for h in host)), "d2h_bytes_per_step": int(d2h[0])},
-        "gpu_launches": args.steps * (2 + (1 if world > 1 else 0)),
+        "gpu_launches": args.steps * ((1 + tree_info["kernels"]) if tree else (2 + (1 if world > 1 else 0))),
         "roofline": roofline,
         "clocks": clk,
         "kernel_resources": info,

@@ -632,6 +632,84 @@ struct ShFwd {
   }
 };
 
+// SH reverse mode: the tree adjoint (tallymap/_reverse_spawn.py:1-45; tree_vjp 233-336).  The reference records
+// every child (rec_primal, 85-109) and runs one adjoint launch per generation, deepest first, so that a parent's
+// replay finds its children's initial-state cotangents ready; here a post-order traversal of each root's tree gives
+// the same order per particle: a particle's children are differentiated before its own steps are transposed.  Per
+// particle the step VJPs run newest first; at the spawn step the children's cotangents enter newest child first
+// (dx1 then dx0), then the deposit's cotangent, then the travel depth' = depth + X0 * L (ct_X0 += ct_depth' * L).
+// Each particle's ct_X0 is one exact emit.  Truncated particles are counted (the gradient is poisoned by the caller).
+struct ShGrad {
+  const float *E0, *d0;
+  const u32* keys;
+  float X0;
+  i32 M;
+  const float* ct;     // [512] cotangent of dep
+  float *gE, *gD;      // [N] cotangents of the roots' E and depth
+  i32* stats;
+  ExactBins* gbins;
+  struct Priv { ExactBins b{1}; i64 trunc = 0, nodes = 0; std::vector<float> buf; };
+  struct StepOut { bool split, low; float z, L, d1; Key kk; };
+  StepOut advance(Key key, i32 k, float E, float depth) const {
+    const Key kk = fold_in(key, (u32)k);
+    const float u0 = uniform_f32(kk, 0u, 0.0f, 1.0f), u1 = uniform_f32(kk, 1u, 0.0f, 1.0f);
+    const float u2 = uniform_f32(kk, 2u, 0.0f, 1.0f);
+    const float L = -tmm::logf(1.0f - u0);
+    const float d1 = depth + X0 * L;
+    const bool low = E < 0.5f;
+    return StepOut{!low && u1 < 0.7f, low, 0.1f + 0.8f * u2, L, d1, kk};
+  }
+  // the adjoint of one particle (and, first, of its subtree): -> the cotangents of its initial E and depth
+  void particle(float E, float depth, Key key, Priv& p, float* dE, float* dD) const {
+    p.nodes += 1;
+    std::vector<float> ds;           // depth before each step
+    i32 kc = 0;
+    bool alive = true, split = false;
+    float d = depth;
+    StepOut last{};
+    while (kc < M && alive) {
+      ds.push_back(d);
+      last = advance(key, kc, E, d);
+      d = last.d1;
+      split = last.split;
+      alive = !last.low && !last.split;
+      kc += 1;
+    }
+    if (kc >= M && alive) p.trunc += 1;
+    float dE1 = 0.0f, dD1 = 0.0f, dE0 = 0.0f, dD0 = 0.0f;
+    if (split) {
+      particle(E * (1.0f - last.z), d, fold_in(last.kk, 1u), p, &dE1, &dD1);
+      particle(E * last.z, d, fold_in(last.kk, 0u), p, &dE0, &dD0);
+    }
+    float ctE = 0.0f, ctd = 0.0f, ctX = 0.0f;
+    for (i32 k = kc - 1; k >= 0; --k) {
+      const StepOut o = advance(key, k, E, ds[k]);
+      if (o.split) {
+        const float f1 = 1.0f - o.z;
+        ctE = ctE + dE1 * f1;
+        ctd = ctd + dD1;
+        ctE = ctE + dE0 * o.z;
+        ctd = ctd + dD0;
+      }
+      if (o.low) {
+        const i32 b = f2i_rz(o.d1 * 8.0f);
+        if ((u32)b < 512u) ctE = ctE + ct[b];
+      }
+      ctX = ctX + ctd * o.L;
+    }
+    exact_emit_priv(p.b, 0, ctX, stats);
+    *dE = ctE;
+    *dD = ctd;
+  }
+  void item(i64 i, Priv& p) const {
+    particle(E0[i], d0[i], Key{keys[2 * i], keys[2 * i + 1]}, p, &gE[i], &gD[i]);
+  }
+  void flush(Priv& p) const {
+    exact_flush(p.b, *gbins, 1, stats);
+    stat_add(stats, 2, (i32)p.trunc);
+  }
+};
+
 }  // namespace
 
 // ================================================================================================= C ABI
@@ -795,6 +873,18 @@ int or_od_grad(i64 n, const float* sigma, const float* rho, const float* y0, con
   p.ctf = ctf; p.ctm = ctm; p.C = C; p.trunc = trunc; p.stats = stats; p.gbins = &gb;
   team_run(p, n, nthreads);
   exact_readout(gb, 1, g, stats);
+  return 0;
+}
+
+// the tree adjoint: g_X0 (exact), g_E[n], g_depth[n]; stats[2] counts truncated particles of the whole forest
+int or_sh_grad(i64 n, const float* E0, const float* d0, const u32* keys, float X0, const float* ct_dep, i32 max_steps,
+               int nthreads, float* g_X0, float* g_E, float* g_depth, i32* stats) {
+  ExactBins gb(1);
+  ShGrad p;
+  p.E0 = E0; p.d0 = d0; p.keys = keys; p.X0 = X0; p.M = max_steps; p.ct = ct_dep;
+  p.gE = g_E; p.gD = g_depth; p.stats = stats; p.gbins = &gb;
+  team_run(p, n, nthreads);
+  exact_readout(gb, 1, g_X0, stats);
   return 0;
 }
 

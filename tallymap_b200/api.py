@@ -55,7 +55,8 @@ FAMILIES = {
     "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
-    "shower": Family("shower", B.SH_FWD, {}, (0, 0, 0, None), 100000),
+    # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
+    "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000),
 }
 
 
@@ -122,7 +123,8 @@ class Mapped:
                 moved.append(a)
         res = self(*moved)
         order = None
-        if isinstance(res.per_item, torch.Tensor) and res.per_item.dtype == torch.int32:
+        if "tree" not in self.fam.grads and isinstance(res.per_item, torch.Tensor) and \
+                res.per_item.dtype == torch.int32:
             order = longest_first(res.per_item)
         return res, self.grad(*moved, wrt=wrt, cotangents=cotangents, order=order)
 
@@ -131,6 +133,8 @@ class Mapped:
         them): ONE replay launch.  cotangents: {output name: array of the output's shape}; missing outputs get zero
         cotangents.  -> a scalar for one index, a vector for a tuple; NaN when an item's replay hit max_steps."""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if "tree" in self.fam.grads:
+            return self._tree_grad(args, idx, cotangents, wrt)
         if any(self.fam.in_axes[w] is not None for w in idx):
             raise ValueError("tallymap_b200: grad with respect to a per-item operand is not built for this item")
         bpos = tuple(sum(1 for ax in self.fam.in_axes[:w] if ax is None) for w in idx)
@@ -152,6 +156,22 @@ class Mapped:
         trunc = out[len(prog.tallies) + 1 + prog.trunc]
         ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
         return ct.reshape(()) if isinstance(wrt, int) else ct
+
+
+    def _tree_grad(self, args, idx, cotangents, wrt):
+        """the gradient of a spawning item through its children (tallymap/_reverse_spawn.py:233-336): the recording
+        forward, then one adjoint launch per generation, deepest first, and one over the roots.  Differentiable
+        arguments: the roots' float per-item operands (-> f32[N]) and the broadcast X0 (-> a scalar)."""
+        pi, bc = self._split(args)
+        c = cotangents.get("dep")
+        ct = torch.zeros(512, dtype=torch.float32) if c is None else c
+        r = self.fam.grads["tree"](pi, bc[0], ct, max_steps=self.max_steps)
+        by_arg = {0: r["ct_E"], 1: r["ct_depth"], 3: r["ct_X0"].reshape(())}
+        if any(w not in by_arg for w in idx):
+            raise ValueError(f"tallymap_b200: item {self.fam.name!r} is differentiable in arguments {sorted(by_arg)}")
+        self.last_tree = r["info"]
+        g = tuple(by_arg[w] for w in idx)
+        return g[0] if isinstance(wrt, int) else g
 
 
 def longest_first(k):

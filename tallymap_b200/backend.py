@@ -72,15 +72,18 @@ class ItemProgram:
     spawns: bool = False
     replay_state_bytes: int = 0     # an adjoint: bytes of one stored loop state in its replay scratch
     queue_leaf_bytes: int = 0       # a spawning program: bytes of one child's leaves in the ring
+    record_bytes: int = 0           # a recording spawning program: bytes of one child's record (tree adjoint)
+    buffers: int = 0                # nonzero: launched by its own driver with this many buffers (not by run())
 
     @property
     def n_args(self):
         return len(self.pi) + len(self.bc) + 2     # + hoisted constants + the optional claim order
 
-    def result_layout(self, N, replay_bytes=0, queue=0):
+    def result_layout(self, N, replay_bytes=0, queue=0, record=0):
         """[(name, nbytes, torch dtype, shape)] of the results, in buffer order, and n_zero.  An adjoint's replay
         scratch (replay_bytes, from replay_plan) comes last and is not zeroed; a spawning program's ring of `queue`
-        slots: its sequence and control words are zeroed (an empty ring), its leaves come last, not zeroed."""
+        slots: its sequence and control words are zeroed (an empty ring), its leaves come last, not zeroed; a
+        recording program's tree counters are zeroed and its `record` slots come after the ring, not zeroed."""
         out = []
         for t in self.tallies:
             out.append((t.name, t.size(N) * _itemsize(t.dtype), t.dtype, t.dims(N)))
@@ -97,6 +100,8 @@ class ItemProgram:
             out.append(("queue.ctl", QCTL_WORDS * 4, torch.int32, (QCTL_WORDS,)))
         out.append(("ctl", CTL_WORDS * 4, torch.int32, (CTL_WORDS,)))
         out.append(("stats", len(STATS) * 4, torch.int32, (len(STATS),)))
+        if self.record_bytes:
+            out.append(("tree", 4 * 8, torch.int64, (4,)))
         n_zero = len(out)
         for y in self.ys:
             out.append((y.name, N * int(np.prod(y.shape, dtype=np.int64)) * _itemsize(y.dtype), y.dtype,
@@ -107,6 +112,9 @@ class ItemProgram:
         if self.queue_leaf_bytes:
             n = max(queue, 1) * self.queue_leaf_bytes // 4
             out.append(("queue.ring", n * 4, torch.int32, (n,)))
+        if self.record_bytes:
+            n = max(record, 1) * self.record_bytes // 4
+            out.append(("record", n * 4, torch.int32, (n,)))
         return out, n_zero
 
 
@@ -167,7 +175,21 @@ SH_FWD = ItemProgram("sh_fwd", "sh_fwd", pi=(Operand("E", (), _F32), Operand("de
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1, spawns=True,
                      queue_leaf_bytes=16)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD, SH_FWD)}
+# its reverse mode (the tree adjoint): the recording forward (the forward's outputs plus every child's record and
+# each root's newest child) and the per-generation adjoint, launched by tree_grad
+SH_PI = (Operand("E", (), _F32), Operand("depth", (), _F32), KEY)
+SH_REC = ItemProgram("sh_rec", "sh_rec", pi=SH_PI, bc=(Operand("X0", (), _F32),), consts=("max_steps", "queue", "record"),
+                     tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32)),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8),
+                         Operand("last", (), torch.int32)), trunc=1, spawns=True, queue_leaf_bytes=24,
+                     record_bytes=32)
+SH_GRAD = ItemProgram("sh_grad", "sh_grad", pi=SH_PI,
+                      bc=(Operand("X0", (), _F32), Operand("ct_dep", (512,), _F32)),
+                      consts=("max_steps", "rev_checkpoints", "replay_threads", "roots", "record"),
+                      tallies=(TSpec("ct_X0", (1,), exact=True),), ys=(), replay_state_bytes=4, buffers=18)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD, SH_FWD, SH_REC,
+                                SH_GRAD)}
 
 
 # -------------------------------------------------------------------------------------------------- run
@@ -233,7 +255,7 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
 
 
 def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, order=None,
-        queue=None, **_):
+        queue=None, record=None, **_):
     """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
     and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
     as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
@@ -265,7 +287,8 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         args.append(t)
     replay_bytes = 0
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
-    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q}
+    R = record_capacity(N, record, dev) if p.record_bytes else 0
+    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q, "record": R}
     if p.replay_state_bytes:
         C, threads, replay_bytes = replay_plan(p, known["max_steps"], rev_checkpoints, dev)
         known.update(rev_checkpoints=C, replay_threads=threads)
@@ -276,8 +299,8 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         if tuple(order.shape) != (N,):
             raise TypeError(f"{p.name}: order has shape {tuple(order.shape)}, expected {(N,)}")
     args.append(order)
-    layout, n_zero = p.result_layout(N, replay_bytes, Q)
-    res = out if out is not None else alloc_results(p, N, dev, replay_bytes, Q)
+    layout, n_zero = p.result_layout(N, replay_bytes, Q, R)
+    res = out if out is not None else alloc_results(p, N, dev, replay_bytes, Q, R)
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
     kid, nbuf = _lib.kernel_id(p.kernel)
@@ -294,6 +317,117 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     return tallies + [res[names.index("stats")]] + list(ys)
 
 
+# The record of a spawning program's reverse mode holds every child ever spawned (a slot is never reused, the
+# reference's condition for a complete record: tallymap/_reverse_spawn.py:30-33).  Its capacity R is the user's
+# `record`, else RECORD_PER_ROOT slots per root (at least RECORD_MIN), at most what RECORD_BUDGET_FRACTION of the free
+# device memory holds at RECORD_SLOT_BYTES per slot (the record, the generation lists and the children's
+# cotangents), below 2^31.  A tree with more children than R is not recorded in full: its gradient is NaN.
+RECORD_PER_ROOT = 16384
+RECORD_MIN = 1 << 20
+RECORD_BUDGET_FRACTION = 0.5
+RECORD_SLOT_BYTES = 32 + 4 + 8
+_RECORD = {}
+
+
+def record_capacity(N, record=None, device=None):
+    if record is not None:
+        R = int(record)
+        if not 1 <= R < 2 ** 31:
+            raise ValueError("tallymap_b200: record capacity must be in [1, 2^31)")
+        return R
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    key = (int(N), dev.index)
+    if key not in _RECORD:
+        free, _ = torch.cuda.mem_get_info(dev)
+        _RECORD[key] = int(max(1, min(2 ** 31 - 1, max(RECORD_MIN, RECORD_PER_ROOT * int(N)),
+                                      RECORD_BUDGET_FRACTION * free // RECORD_SLOT_BYTES)))
+    return _RECORD[key]
+
+
+TREE_MAX_GEN = 1024     # generations the tree adjoint takes (deeper trees: NaN gradient, counted)
+
+
+def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):
+    """Reverse mode through spawn for the shower (tallymap/_reverse_spawn.py:233-336, tree_vjp): the recording
+    forward (rec_primal), the generation lists (tm_tree_generations), then one adjoint launch per generation,
+    deepest first, and one over the roots.  Each adjoint item replays its particle and injects its children's
+    initial-state cotangents (from the previous launch) at the spawn step.
+    -> dict(forward=[dep, count, stats, k, truncated] as run() returns them, ct_X0 f32[1], ct_E f32[N],
+            ct_depth f32[N], words (ct_X0's exact scratch words, for a cross-GPU combine), info={children,
+            generations, launches (the reference's count: the recording primal + one per generation + the roots'),
+            kernels (launches of this backend's kernels), record, poisoned (device bool), ...})
+    Every cotangent is NaN when the record is incomplete (a child dropped or past the record's capacity, a
+    generation deeper than TREE_MAX_GEN), when a replay disagrees with the record, or when any particle hit
+    max_steps."""
+    import ctypes
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    fwd = run(SH_REC, pi, [X0], consts=(max_steps,), queue=queue, record=record, stream=st)
+    last = run.last
+    res, args = last["results"], last["args"]
+    R = int(last["consts"][SH_REC.consts.index("record")])
+    N = int(args[0].shape[0])
+    rec, root_last, stats = res["record"], res["last"], res["stats"]
+    head = torch.cat([res["tree"][:1], stats.to(torch.int64)]).cpu()        # (one sync)
+    total, dropped = int(head[0]), int(head[1 + STATS.index("children_dropped")])
+    n_rec = min(total, R)
+    L = _lib.lib()
+    counts = torch.empty(TREE_MAX_GEN + 1, dtype=torch.int64, device=dev)
+    cursor = torch.empty_like(counts)
+    lists = torch.empty(max(n_rec, 1), dtype=torch.int32, device=dev)
+    _lib.check(L.tm_tree_generations(ctypes.c_void_p(st), ctypes.c_void_p(rec.data_ptr()), n_rec,
+                                     SH_REC.record_bytes, 24, TREE_MAX_GEN, ctypes.c_void_p(counts.data_ptr()),
+                                     ctypes.c_void_p(cursor.data_ptr()), ctypes.c_void_p(lists.data_ptr())))
+    cnt = counts.cpu().numpy()                                              # (second sync)
+    offs = np.concatenate([[0], np.cumsum(cnt)])
+    nz = np.nonzero(cnt[:TREE_MAX_GEN])[0]
+    G = int(nz.max()) if len(nz) else 0
+    incomplete = total > R or dropped > 0 or cnt[TREE_MAX_GEN] > 0
+
+    # the adjoint launches: [E0, depth0, keys, X0, ct_dep, record, last, consts, order] | [ctl, ct_X0, exact words,
+    # stats, tree counters, ct_E, ct_depth, dx, replay scratch]
+    C, threads, replay_bytes = replay_plan(SH_GRAD, max_steps, rev_checkpoints, dev)
+    x0 = args[3]
+    ctd = _dev(ct_dep, dev, _F32).reshape(-1)
+    if ctd.numel() != 512:
+        raise TypeError("tallymap_b200: ct_dep must have 512 elements")
+    outs = [torch.empty(CTL_WORDS, dtype=torch.int32, device=dev), torch.empty(1, dtype=_F32, device=dev),
+            torch.empty(EXACT_WORDS + 1, dtype=torch.int64, device=dev),
+            torch.empty(len(STATS), dtype=torch.int32, device=dev), torch.empty(4, dtype=torch.int32, device=dev),
+            torch.empty(N, dtype=_F32, device=dev), torch.empty(N, dtype=_F32, device=dev),
+            torch.empty(max(n_rec, 1) * 2, dtype=_F32, device=dev),
+            torch.empty(max(1, (replay_bytes + 15) // 16) * 4, dtype=torch.int32, device=dev)]
+    nbytes = [t.numel() * t.element_size() for t in outs]
+    kid, nbuf = _lib.kernel_id(SH_GRAD.kernel)
+    base = [args[0], args[1], args[2], x0, ctd, rec, root_last]
+    launches = 0
+    if not incomplete:
+        for g in list(range(G, 0, -1)) + [0]:
+            n = N if g == 0 else int(cnt[g])
+            if n == 0:
+                continue
+            # (the adjoint bounds child slots by the recorded count, not the capacity: no slot past it was written)
+            cst = _consts((int(max_steps), C, threads, 1 if g == 0 else 0, max(n_rec, 1)), dev)
+            order = 0 if g == 0 else lists.data_ptr() + 4 * int(offs[g])
+            ptrs = [t.data_ptr() for t in base] + [cst.data_ptr(), order] + [t.data_ptr() for t in outs]
+            assert len(ptrs) == nbuf == SH_GRAD.buffers
+            _lib.launch(kid, st, ptrs, 9, nbytes, 5 if launches == 0 else 1, n, flags=8)
+            launches += 1
+    if launches == 0:
+        for t in outs[:5]:
+            t.zero_()
+    ctX, ctE, ctD, tree = outs[1], outs[5], outs[6], outs[4]
+    trunc = fwd[4]
+    bad = (tree[0] > 0) | (tree[1] > 0) | (stats[2] > 0) | trunc.bool().any() | bool(incomplete)
+    nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
+    tree_grad.last = dict(ctl=outs[0], fwd_ctl=last["ctl"])
+    return dict(forward=fwd[:5], ct_X0=nan(ctX), ct_E=nan(ctE), ct_depth=nan(ctD),
+                words=outs[2], stats=outs[3],
+                info=dict(children=total, generations=G, launches=launches + 2, kernels=launches + 4, record=R,
+                          poisoned=bad,
+                          mismatch=tree[0], replay_truncated=tree[1], generation_sizes=cnt[:G + 1].tolist()))
+
+
 _CONSTS = {}
 
 
@@ -307,14 +441,15 @@ def _consts(vals, dev):
     return t
 
 
-def alloc_results(p, N, device=None, replay_bytes=None, queue=None):
+def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None):
     """result buffers for N items (an adjoint's replay scratch as planned on `device` unless given; a spawning
-    program's ring of `queue` slots)."""
+    program's ring of `queue` slots; a recording program's `record` slots)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     if replay_bytes is None and p.replay_state_bytes:
         replay_bytes = replay_plan(p, 2 ** 31 - 1, None, device)[2]
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
-    layout, _ = p.result_layout(N, replay_bytes or 0, Q)
+    R = record_capacity(N, record, device) if p.record_bytes else 0
+    layout, _ = p.result_layout(N, replay_bytes or 0, Q, R)
     return [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout]
 
 

@@ -44,6 +44,28 @@ struct ShowerState {
   bool alive;
 };
 
+// The loop body above, shared by the forward, the recording forward and the adjoint's replay: travel, the deposit
+// when low (emitted through `emit` unless null), the split decision.  -> the split flag, the energy fraction z of
+// child 0 and the step key (the children's keys are fold_in(kk, 0) and fold_in(kk, 1)).
+struct ShowerStepOut {
+  bool split, low;
+  float z, L;
+  Key kk;
+};
+template <class St>
+__device__ __forceinline__ ShowerStepOut shower_advance(float X0, St& s) {
+  const Key kk = fold_in(s.key, (u32)s.k);
+  const float u0 = uniform01(kk, 0u), u1 = uniform01(kk, 1u), u2 = uniform01(kk, 2u);
+  const float L = -tmm::logf(1.0f - u0);
+  s.depth = s.depth + X0 * L;
+  const bool low = s.E < 0.5f;
+  const bool split = !low && u1 < 0.7f;
+  s.alive = !low && !split;
+  s.kc += 1;
+  s.k += 1;
+  return ShowerStepOut{split, low, 0.1f + 0.8f * u2, L, kk};
+}
+
 struct SHFwd {
   enum { kE0, kDepth0, kKeys, kX0, kConsts, kOrder, kDep, kCount, kSeq, kQctl, kCtl, kStats, kK, kTrunc, kQueue,
          kNBuf };
@@ -89,22 +111,14 @@ struct SHFwd {
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
   __device__ __forceinline__ static void step(const Ctx& c, State& s, Child* out, int* n_out) {
-    const Key kk = fold_in(s.key, (u32)s.k);
-    const float u0 = uniform01(kk, 0u), u1 = uniform01(kk, 1u), u2 = uniform01(kk, 2u);
-    s.depth = s.depth + c.X0 * (-tmm::logf(1.0f - u0));
-    const bool low = s.E < 0.5f;
-    SumPriv<kNB>::emit(c.sh, c.stats, low ? f2i(s.depth * 8.0f) : 0, low ? s.E : 0.0f);
-    const bool split = !low && u1 < 0.7f;
-    if (split) {
-      const float z = 0.1f + 0.8f * u2;
-      const Key c0 = fold_in(kk, 0u), c1 = fold_in(kk, 1u);
-      out[0] = Child{s.E * z, s.depth, c0.a, c0.b};
-      out[1] = Child{s.E * (1.0f - z), s.depth, c1.a, c1.b};
+    const ShowerStepOut o = shower_advance(c.X0, s);
+    if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
+    if (o.split) {
+      const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
+      out[0] = Child{s.E * o.z, s.depth, c0.a, c0.b};
+      out[1] = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
       *n_out = 2;
     }
-    s.alive = !low && !split;
-    s.kc += 1;
-    s.k += 1;
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {
     atomicAdd(c.shc, 1);                                   // count: Sum((1,)) int32, privatised
@@ -124,6 +138,293 @@ struct SHFwd {
     }
   }
   __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
+// ------------------------------------------------------------------------------------ reverse mode: the tree adjoint
+// The reference differentiates through spawn with a recording primal and one adjoint launch per generation
+// (tallymap/_reverse_spawn.py:1-45): the record holds every child's initial state, parent, ordinal and generation;
+// the adjoint of generation g replays each of its items and injects, at the spawn step, the cotangents of the
+// children's initial states computed by generation g + 1's launch.
+//
+// Record of a child (one 32-byte sector per slot; slots from a warp-aggregated counter, never reused):
+//   E, depth, key   its initial state (the leaves the ring carries)
+//   prev            the slot of its parent's previous child (-1: none), so a parent's children form a chain
+//                   from its newest child backwards: the order in which the parent's adjoint consumes them
+//   last            its own newest child (-1: none), written when it finishes
+//   gen             its generation (a root's children are generation 1)
+// A root's newest child goes to the per-item result `last`.  With the chains, the adjoint reaches a parent's children
+// without the reference's (parent, ordinal) sort of every generation (_reverse_spawn.py:255-283); the generation
+// lists only decide launch order.  A slot past the record's capacity R is not written; the host then poisons the
+// gradient (the reference's 'drop_risk', _reverse_spawn.py:30-33).
+struct __align__(16) ShowerRecord {
+  float E, depth;
+  u32 ka, kb;
+  i32 prev, last, gen, pad;
+};
+
+struct ShowerRecChild {
+  float E, depth;
+  u32 ka, kb;
+  i32 slot, gen;
+};
+
+struct ShowerRecState {
+  i32 kc, k;
+  float E, depth;
+  Key key;
+  bool alive;
+  i32 me, gen, last;   // me: own record slot (a child) or -1 (a root)
+};
+
+// the recording forward (rec_primal, _reverse_spawn.py:85-109): the forward's outputs, plus the record.
+//   sh_rec   E0 f32[N], depth0 f32[N], keys u32[N,2], X0 f32, consts i32[3] (max_steps, Q, R), order |
+//            dep f32[512], count i32[1], seq u32[Q], qctl u32[5*32], ctl, stats, tree u64[4] (0: children
+//            recorded or not) | k i32[N], trunc u8[N], last i32[N], ring ShowerRecChild[Q], record ShowerRecord[R]
+struct SHRec {
+  enum { kE0, kDepth0, kKeys, kX0, kConsts, kOrder, kDep, kCount, kSeq, kQctl, kCtl, kStats, kTree, kK, kTrunc,
+         kLast, kQueue, kRecord, kNBuf };
+  enum { kConstM, kConstQ, kConstR };
+  static constexpr int kNB = 512;
+  static constexpr int kSmemBytes = kNB * 4 + 16;
+  typedef ShowerRecChild Child;
+  typedef ShowerRecState State;
+  struct Ctx {
+    const float *E0, *d0;
+    const uint2* keys;
+    float X0;
+    i32 M;
+    u64 R;
+    float* sh;
+    i32* shc;
+    float* dep;
+    i32* count;
+    i32* stats;
+    u64* tree;
+    i32* kout;
+    uint8_t* trunc;
+    i32* lastout;
+    ShowerRecord* rec;
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    const i32* consts = static_cast<const i32*>(P.p[kConsts]);
+    c.E0 = static_cast<const float*>(P.p[kE0]);
+    c.d0 = static_cast<const float*>(P.p[kDepth0]);
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.X0 = __ldg(static_cast<const float*>(P.p[kX0]));
+    c.M = __ldg(consts + kConstM);
+    c.R = (u64)(u32)__ldg(consts + kConstR);
+    c.sh = reinterpret_cast<float*>(smem);
+    c.shc = reinterpret_cast<i32*>(smem + kNB * 4);
+    c.dep = static_cast<float*>(P.p[kDep]);
+    c.count = static_cast<i32*>(P.p[kCount]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.tree = static_cast<u64*>(P.p[kTree]);
+    c.kout = static_cast<i32*>(P.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.lastout = static_cast<i32*>(P.p[kLast]);
+    c.rec = static_cast<ShowerRecord*>(P.p[kRecord]);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true, -1, 0, -1};
+  }
+  __device__ static State start_child(Ctx&, const Child& ch) {
+    return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true, ch.slot, ch.gen, -1};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child* out, int* n_out) {
+    const ShowerStepOut o = shower_advance(c.X0, s);
+    if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
+    // record slots for the children of this iteration's splitting lanes: one atomic per warp
+    const unsigned m = __activemask();
+    const unsigned ms = __ballot_sync(m, o.split);
+    if (o.split) {
+      const int lane = threadIdx.x & 31;
+      const int leader = __ffs(ms) - 1;
+      unsigned long long base = 0ull;
+      if (lane == leader) base = atomicAdd(reinterpret_cast<unsigned long long*>(c.tree), 2ull * __popc(ms));
+      base = __shfl_sync(ms, base, leader) + 2ull * __popc(ms & ((1u << lane) - 1u));
+      const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
+      const float e0 = s.E * o.z, e1 = s.E * (1.0f - o.z);
+      const i32 r0 = (u64)base < c.R ? (i32)base : -1;
+      const i32 r1 = (u64)base + 1 < c.R ? (i32)(base + 1) : -1;
+      if (r0 >= 0) c.rec[r0] = ShowerRecord{e0, s.depth, c0.a, c0.b, s.last, -1, s.gen + 1, 0};
+      if (r1 >= 0) c.rec[r1] = ShowerRecord{e1, s.depth, c1.a, c1.b, r0, -1, s.gen + 1, 0};
+      s.last = r1;
+      out[0] = Child{e0, s.depth, c0.a, c0.b, r0, s.gen + 1};
+      out[1] = Child{e1, s.depth, c1.a, c1.b, r1, s.gen + 1};
+      *n_out = 2;
+    }
+  }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {
+    atomicAdd(c.shc, 1);
+    const bool tr = s.kc >= c.M && s.alive;
+    if (child) {
+      if (tr) atomicAdd(&c.stats[kStChildrenTruncated], 1);
+      if (s.me >= 0) c.rec[s.me].last = s.last;
+    } else {
+      c.kout[item] = s.k;
+      c.trunc[item] = tr ? 1 : 0;
+      c.lastout[item] = s.last;
+    }
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.dep, tid, nth);
+    if (tid == 0) {
+      const i32 v = *reinterpret_cast<const i32*>(smem + kNB * 4);
+      if (v) atomicAdd(c.count, v);
+    }
+  }
+  __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
+// The adjoint of one generation (or of the roots): replay_kernel over the generation's record slots (the claim order
+// is the generation's list) or over the root items.  Per particle, newest step first: the children's cotangents
+// (dx of the newest child first, following the chain), the deposit's cotangent ct_dep[bin] into E, then the travel
+// depth' = depth + X0 * L: ct_X0 += ct_depth' * L.  The particle's initial-state cotangent goes to dx[slot] (a child)
+// or to the per-item results g_E, g_depth (a root); ct_X0 is an exact tally.  Replay consistency
+// (_reverse_spawn.py:22-26): a child slot must exist where the replay spawns and hold exactly the state the replay
+// spawns, and the chain must end with the particle's last spawn; otherwise tree[0] counts a mismatch and the host
+// poisons the gradient.
+//   sh_grad  E0 f32[N], depth0 f32[N], keys u32[N,2], X0 f32, ct_dep f32[512], record ShowerRecord[R], last i32[N],
+//            consts i32[5] (max_steps, C, threads, roots, R), order (the generation's slots) |
+//            ctl, g_X0 f32[1], exact words, stats, tree u32[4] | g_E f32[N], g_depth f32[N], dx float2[R], replay
+struct SHGrad {
+  enum { kE0, kDepth0, kKeys, kX0, kCtDep, kRecord, kRootLast, kConsts, kOrder, kCtl, kGX0, kExact, kStats, kTree,
+         kGE, kGDepth, kDx, kReplay, kNBuf };
+  enum { kConstM, kConstC, kConstThreads, kConstRoots, kConstR };
+  static constexpr int kNB = 512;
+  static constexpr int kSmemBytes = ExactBins<1>::kSmemBytes + kNB * 4;
+  typedef ShowerState State;
+  struct Ctx {
+    const float *E0, *d0;
+    const uint2* keys;
+    float X0;
+    i32 M;
+    bool roots;
+    i32 R;
+    const float* ct;
+    const ShowerRecord* rec;
+    const i32* root_last;
+    float2* dx;
+    float *gE, *gD;
+    u64* gw;
+    float* g;
+    i32* stats;
+    u32* tree;
+    Key key;           // the current item's key, energy and newest child
+    float E;
+    i32 last;
+    mutable ExactPriv<1> pv;
+  };
+  struct Adj {
+    float ctE, ctd, ctX;
+    i32 cur;           // the next child to consume (newest first)
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    const i32* consts = static_cast<const i32*>(P.p[kConsts]);
+    c.E0 = static_cast<const float*>(P.p[kE0]);
+    c.d0 = static_cast<const float*>(P.p[kDepth0]);
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.X0 = __ldg(static_cast<const float*>(P.p[kX0]));
+    c.M = __ldg(consts + kConstM);
+    c.roots = __ldg(consts + kConstRoots) != 0;
+    c.R = __ldg(consts + kConstR);
+    c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
+    c.rec = static_cast<const ShowerRecord*>(P.p[kRecord]);
+    c.root_last = static_cast<const i32*>(P.p[kRootLast]);
+    c.dx = static_cast<float2*>(P.p[kDx]);
+    c.gE = static_cast<float*>(P.p[kGE]);
+    c.gD = static_cast<float*>(P.p[kGDepth]);
+    c.gw = static_cast<u64*>(P.p[kExact]);
+    c.g = static_cast<float*>(P.p[kGX0]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.tree = static_cast<u32*>(P.p[kTree]);
+    c.pv.zero();
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    const float* ct = static_cast<const float*>(P.p[kCtDep]);
+    float* d = reinterpret_cast<float*>(smem + ExactBins<1>::kSmemBytes);
+    for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    float E, d;
+    if (c.roots) {
+      const uint2 kk = __ldg(&c.keys[item]);
+      c.key = Key{kk.x, kk.y};
+      E = __ldg(&c.E0[item]);
+      d = __ldg(&c.d0[item]);
+      c.last = __ldg(&c.root_last[item]);
+    } else {
+      const ShowerRecord r = c.rec[item];
+      c.key = Key{r.ka, r.kb};
+      E = r.E;
+      d = r.depth;
+      c.last = r.last;
+    }
+    c.E = E;
+    return State{0, 0, E, d, c.key, true};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
+  __device__ static void adj_start(const Ctx& c, Adj& a) { a = Adj{0.0f, 0.0f, 0.0f, c.last}; }
+  typedef float Stored;   // a stored state is alive with the item's E and key: only depth varies
+  __device__ __forceinline__ static Stored store(const State& s) { return s.depth; }
+  __device__ __forceinline__ static State restore(const Ctx& c, Stored d, i64 step) {
+    return State{(i32)step, (i32)step, c.E, d, c.key, true};
+  }
+  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) { shower_advance(c.X0, s); }
+  // one recorded child for the spawn being transposed: its initial-state cotangent, after checking that the record
+  // holds what the replay spawns; advances the chain
+  __device__ __forceinline__ static float2 child_ct(const Ctx& c, Adj& a, float E, float depth, Key k) {
+    const i32 r = a.cur;
+    if (r < 0 || r >= c.R) {
+      atomicAdd(&c.tree[0], 1u);
+      return make_float2(0.0f, 0.0f);
+    }
+    const ShowerRecord rc = c.rec[r];
+    if (__float_as_uint(rc.E) != __float_as_uint(E) || __float_as_uint(rc.depth) != __float_as_uint(depth) ||
+        rc.ka != k.a || rc.kb != k.b)
+      atomicAdd(&c.tree[0], 1u);
+    a.cur = rc.prev;
+    return c.dx[r];
+  }
+  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {
+    State s = at;
+    const ShowerStepOut o = shower_advance(c.X0, s);
+    if (o.split) {
+      const float f1 = 1.0f - o.z;
+      const float2 d1 = child_ct(c, a, at.E * f1, s.depth, fold_in(o.kk, 1u));
+      a.ctE = a.ctE + d1.x * f1;
+      a.ctd = a.ctd + d1.y;
+      const float2 d0 = child_ct(c, a, at.E * o.z, s.depth, fold_in(o.kk, 0u));
+      a.ctE = a.ctE + d0.x * o.z;
+      a.ctd = a.ctd + d0.y;
+    }
+    if (o.low) {
+      const i32 b = f2i(s.depth * 8.0f);
+      if ((u32)b < (u32)kNB) a.ctE = a.ctE + c.ct[b];
+    }
+    a.ctX = a.ctX + a.ctd * o.L;
+  }
+  __device__ static void post_vjp(const Ctx&, const State&, Adj&) {}
+  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {
+    if (a.cur != -1) atomicAdd(&c.tree[0], 1u);           // recorded children the replay did not spawn
+    if (fin.kc >= c.M && fin.alive) atomicAdd(&c.tree[1], 1u);
+    if (c.roots) {
+      c.gE[item] = a.ctE;
+      c.gD[item] = a.ctd;
+    } else {
+      c.dx[item] = make_float2(a.ctE, a.ctd);
+    }
+    if (c.pv.emit(0, a.ctX)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+  }
+  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
+    ExactBins<1>::flush(c.pv, smem, c.gw, c.stats, tid);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
+    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
+  }
 };
 
 }  // namespace tmb

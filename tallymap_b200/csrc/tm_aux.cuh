@@ -2,6 +2,8 @@
 //   exact_combine_kernel   the cross-GPU step of an exact (TSpec.exact) tally: every rank's carry-save words for a
 //                          bin, gathered, are added with their carries and read out once, correctly rounded
 //   exact_scatter_kernel   an exact f32 scatter-add of (value, bin) pairs (the exact Sum accumulator on its own)
+//   tree_hist_kernel, tree_scan_kernel, tree_scatter_kernel
+//                          the generation lists of a recorded spawn tree (the launch order of the tree adjoint)
 //   probe_threefry_kernel  the calibration probe of the roofline: threefry2x32 evaluations per second at full
 //                          occupancy with no memory traffic (the issue-rate peak of the walkers' dominant op mix)
 #pragma once
@@ -77,6 +79,57 @@ __global__ void exact_readout_kernel(const u64* words, int n_bins, float* out, i
 }
 
 // the backend's f32 math on the device, elementwise (fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y))
+// ---- generation lists of a recorded spawn tree.  The reference orders each generation of the record with XLA
+// scatters and a while loop (tallymap/_reverse_spawn.py:255-283) and launches the adjoint one generation at a time.
+// Records are `stride` bytes apart with an int32 generation at byte `gen_off`; generations >= n_gen (or < 0) are
+// counted in counts[n_gen] and listed nowhere (the host poisons the gradient: the reference's
+// 'generation_overflow').  Within a generation the list order is arbitrary (a warp-aggregated cursor per
+// generation): each adjoint item writes only its own slot, and broadcast cotangents are exact tallies.
+__device__ __forceinline__ int tree_gen_of(const unsigned char* rec, long long r, int stride, int gen_off,
+                                           int n_gen) {
+  const int g = *reinterpret_cast<const int*>(rec + r * stride + gen_off);
+  return (g >= 0 && g < n_gen) ? g : n_gen;
+}
+
+// counts[g] += the records of generation g (shared-memory histogram of n_gen + 1 bins per block)
+__global__ void tree_hist_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int n_gen,
+                                 unsigned long long* counts) {
+  extern __shared__ u32 hist[];
+  for (int i = threadIdx.x; i <= n_gen; i += blockDim.x) hist[i] = 0u;
+  __syncthreads();
+  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x)
+    atomicAdd(&hist[tree_gen_of(rec, r, stride, gen_off, n_gen)], 1u);
+  __syncthreads();
+  for (int i = threadIdx.x; i <= n_gen; i += blockDim.x)
+    if (hist[i]) atomicAdd(&counts[i], (unsigned long long)hist[i]);
+}
+
+// cursor[g] = the exclusive prefix sum of counts (one thread: n_gen is a few thousand at most)
+__global__ void tree_scan_kernel(const unsigned long long* counts, int n_gen, unsigned long long* cursor) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  unsigned long long a = 0ull;
+  for (int g = 0; g <= n_gen; ++g) {
+    cursor[g] = a;
+    a += counts[g];
+  }
+}
+
+// lists[cursor[g]++] = r for every record r of generation g < n_gen (lanes of a warp with the same generation share
+// one atomic)
+__global__ void tree_scatter_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int n_gen,
+                                   unsigned long long* cursor, i32* lists) {
+  const int lane = threadIdx.x & 31;
+  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x) {
+    const int g = tree_gen_of(rec, r, stride, gen_off, n_gen);
+    const unsigned peers = __match_any_sync(__activemask(), g);
+    const int leader = __ffs(peers) - 1;
+    unsigned long long base = 0ull;
+    if (lane == leader) base = atomicAdd(&cursor[g], (unsigned long long)__popc(peers));
+    base = __shfl_sync(peers, base, leader);
+    if (g < n_gen) lists[base + __popc(peers & ((1u << lane) - 1u))] = (i32)r;
+  }
+}
+
 __global__ void math_eval_kernel(int fn, const float* x, const float* y, float* out, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float a = x[i];

@@ -109,6 +109,8 @@ void init_registry() {
   add_forward<tmb::ODFwd>("od_fwd");
   add_replay<tmb::ODGrad, 1>("od_grad");
   add_spawn<tmb::SHFwd>("sh_fwd");
+  add_spawn<tmb::SHRec>("sh_rec");
+  add_replay<tmb::SHGrad, 1>("sh_grad");
 }
 
 Kernel* find(int64_t id) {
@@ -370,6 +372,37 @@ int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bin
                                                                   stats);
   e = cudaGetLastError();
   return e == cudaSuccess ? TM_OK : cuda_fail("exact_readout_kernel", e);
+}
+
+int tm_tree_generations(void* stream, const void* records, int64_t n_records, int32_t record_bytes,
+                        int32_t gen_offset, int32_t n_gen, uint64_t* counts, uint64_t* cursor, int32_t* lists) {
+  if (n_records < 0 || n_records > INT32_MAX || record_bytes < 4 || record_bytes % 4 || gen_offset < 0 ||
+      gen_offset % 4 || gen_offset + 4 > record_bytes || n_gen < 1 || n_gen > TM_TREE_MAX_GEN || !counts ||
+      !cursor || (n_records > 0 && (!records || !lists)))
+    return fail(TM_EINVAL, "tallymap_b200: tm_tree_generations: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)(n_gen + 1) * 8, st);
+  if (e != cudaSuccess) return cuda_fail("cudaMemsetAsync", e);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  long long grid = (n_records + 255) / 256;
+  if (grid > 8LL * sms) grid = 8LL * sms;
+  if (grid < 1) grid = 1;
+  const unsigned char* rec = static_cast<const unsigned char*>(records);
+  unsigned long long* const cnt = reinterpret_cast<unsigned long long*>(counts);
+  unsigned long long* const cur = reinterpret_cast<unsigned long long*>(cursor);
+  tmb::tree_hist_kernel<<<(unsigned)grid, 256, (size_t)(n_gen + 1) * 4, st>>>(rec, n_records, record_bytes,
+                                                                               gen_offset, n_gen, cnt);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_hist_kernel", e);
+  tmb::tree_scan_kernel<<<1, 32, 0, st>>>(cnt, n_gen, cur);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_scan_kernel", e);
+  if (n_records > 0) {
+    tmb::tree_scatter_kernel<<<(unsigned)grid, 256, 0, st>>>(rec, n_records, record_bytes, gen_offset, n_gen, cur,
+                                                             lists);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_scatter_kernel", e);
+  }
+  return TM_OK;
 }
 
 int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used) {

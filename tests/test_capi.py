@@ -38,6 +38,9 @@ def test_builtin_kernels(tmlib):
     from tallymap_b200 import backend as B
     for p in B.PROGRAMS.values():
         kid, nbuf = tmlib.kernel_id(p.kernel)
+        if p.buffers:                                       # launched by its own driver (backend.tree_grad)
+            assert nbuf == p.buffers, p.name
+            continue
         layout, n_zero = p.result_layout(10)
         assert nbuf == p.n_args + len(layout), p.name       # the Python layout matches the kernel's
 

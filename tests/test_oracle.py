@@ -141,3 +141,18 @@ def test_empty(orc):
     assert r["hist"].sum() == 0 and r["k"].size == 0
     g = orc.rw_grad(x, k, 1.0, np.ones(256, np.float32))
     assert g["g"][0] == 0.0
+
+
+def test_oracle_sh_grad_energy(orc):
+    """the oracle's tree adjoint: with ct_dep = 1 each root's E cotangent is the share of its energy that lands in
+    range (1 up to rounding: children split E into z E and (1 - z) E), and X0 and depth get none (they only move
+    integer bins)"""
+    inp = orc.sh_inputs(200, seed=4)
+    g = orc.sh_grad(*inp)
+    assert np.median(np.abs(g["g_E"] - 1.0)) < 1e-5 and np.abs(g["g_E"] - 1.0).max() < 1e-2
+    assert g["g_X0"][0] == 0.0 and not g["g_depth"].any()
+    ct = np.random.default_rng(2).normal(size=512).astype(np.float32)
+    g2 = orc.sh_grad(*inp, ct_dep=ct)
+    # linearity in the cotangent
+    g3 = orc.sh_grad(*inp, ct_dep=2 * ct)
+    assert np.allclose(g3["g_E"], 2 * g2["g_E"], rtol=1e-6, atol=1e-6)

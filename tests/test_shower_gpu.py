@@ -60,3 +60,77 @@ def test_sh_full_size(cuda, orc):
     assert int(a["count"][0]) == 1048576 + int(a["stats"][0]) and a["stats"][1] == 0
     e0 = float(inp[0].astype(np.float64).sum())
     assert abs(float(a["dep"].astype(np.float64).sum()) - e0) <= 1e-3 * e0
+
+
+# ---------------------------------------------------------------------------------------------- the tree adjoint
+def gpu_sh_grad(inp, X0=1.0, ct=None, M=100000, Q=None, R=None):
+    ct = np.ones(512, np.float32) if ct is None else ct
+    r = B.tree_grad(list(inp), np.float32(X0), ct, max_steps=M, queue=Q, record=R)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    B.check_status(B.tree_grad.last["ctl"])
+    out = {k: r[k].cpu().numpy() for k in ("ct_X0", "ct_E", "ct_depth")}
+    out["info"] = r["info"]
+    out["poisoned"] = bool(r["info"]["poisoned"].item())
+    out["mismatch"] = int(r["info"]["mismatch"].item())
+    out["fwd"] = [o.cpu().numpy() for o in r["forward"]]
+    return out
+
+
+@pytest.mark.parametrize("n", [1, 300, 3000])
+def test_sh_tree_grad(cuda, orc, n):
+    """the per-generation adjoint launches against the oracle's post-order traversal: every root's E and depth
+    cotangent bitwise, the X0 cotangent (an exact tally) bitwise; the recording forward's outputs as the forward's"""
+    inp = orc.sh_inputs(n, seed=7)
+    ct = np.random.default_rng(n).normal(size=512).astype(np.float32)
+    ref = orc.sh_grad(*inp, ct_dep=ct)
+    got = gpu_sh_grad(inp, ct=ct)
+    assert not got["poisoned"] and got["mismatch"] == 0
+    assert np.array_equal(got["ct_E"].view(np.uint32), ref["g_E"].view(np.uint32))
+    assert np.array_equal(got["ct_depth"].view(np.uint32), ref["g_depth"].view(np.uint32))
+    assert np.array_equal(got["ct_X0"].view(np.uint32), ref["g_X0"].view(np.uint32))
+    fr = orc.sh_fwd(*inp)
+    dep, count, stats, k, tr = got["fwd"]
+    assert np.array_equal(count, fr["count"]) and np.array_equal(stats, fr["stats"])
+    assert np.array_equal(k, fr["k"]) and np.array_equal(tr.astype(bool), fr["trunc"])
+    assert got["info"]["children"] == int(fr["stats"][0])
+    assert sum(got["info"]["generation_sizes"]) == int(fr["stats"][0])
+    assert got["info"]["launches"] == 2 + sum(1 for c in got["info"]["generation_sizes"][1:] if c) + 1
+
+
+def test_sh_tree_grad_energy(cuda, orc):
+    """with ct_dep = 1 a root's E cotangent is the fraction of its energy deposited in range: 1 up to rounding for
+    every root whose tree stays within depth 64"""
+    inp = orc.sh_inputs(5000, seed=9)
+    got = gpu_sh_grad(inp)
+    assert not got["poisoned"]
+    assert np.abs(got["ct_E"] - 1.0).max() < 1e-2 and np.median(np.abs(got["ct_E"] - 1.0)) < 1e-5
+    assert float(got["ct_X0"][0]) == 0.0 and not got["ct_depth"].any()
+
+
+@pytest.mark.parametrize("how", ["record", "ring", "steps"])
+def test_sh_tree_grad_poison(cuda, orc, how):
+    """an incomplete record (capacity below the children, or children dropped by a small ring) or a truncated
+    particle poisons every cotangent (tallymap/_reverse_spawn.py:30-38); the forward outputs stay as they are"""
+    inp = orc.sh_inputs(2000, seed=3)
+    kw = dict(record=dict(R=1000), ring=dict(Q=64), steps=dict(M=1))[how]
+    got = gpu_sh_grad(inp, **kw)
+    assert got["poisoned"]
+    assert np.isnan(got["ct_E"]).all() and np.isnan(got["ct_X0"]).all() and np.isnan(got["ct_depth"]).all()
+    if how == "record":
+        ref = orc.sh_fwd(*inp)
+        assert np.array_equal(got["fwd"][1], ref["count"]) and got["info"]["children"] == int(ref["stats"][0])
+
+
+def test_sh_tree_grad_full_size(cuda, orc):
+    """N = 1,048,576 roots (~10^9 recorded children): repeatable bitwise, energy-conserving E cotangents"""
+    inp = orc.sh_inputs(1048576)
+    a = gpu_sh_grad(inp)
+    b = gpu_sh_grad(inp)
+    assert not a["poisoned"] and a["mismatch"] == 0
+    assert np.array_equal(a["ct_E"].view(np.uint32), b["ct_E"].view(np.uint32))
+    assert np.array_equal(a["ct_X0"].view(np.uint32), b["ct_X0"].view(np.uint32))
+    assert np.median(np.abs(a["ct_E"] - 1.0)) < 1e-5
+    idx = np.random.default_rng(0).choice(1048576, 64, replace=False)
+    ref = orc.sh_grad(inp[0][idx], inp[1][idx], inp[2][idx])
+    assert np.array_equal(a["ct_E"][idx].view(np.uint32), ref["g_E"].view(np.uint32))
