@@ -290,7 +290,7 @@ def main():
     ct = [torch.ones((N, 3), device=dev) if isinstance(c, str) else torch.tensor(c, device=dev) for c in cfg.ct]
     tree = cfg.name == "sh"
     fo = B.alloc_results(cfg.fwd, N, dev)
-    go = None if tree else B.alloc_results(cfg.grad, N, dev)
+    go = None if tree else B.alloc_results(cfg.grad, N, dev, max_steps=cfg.max_steps)
     nb = cfg.grad.tallies[0].S
     g_all = torch.zeros(nb, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)

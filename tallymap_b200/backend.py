@@ -215,11 +215,14 @@ def _dev(x, device, dtype):
 
 # The replay's checkpoint count C (the reference's rev_checkpoints option, tallymap/_reverse.py:116-134).  Any C gives
 # bitwise the same cotangents; C only trades memory for replay work.  The reference picks C from the logical state
-# size (16 for small steps) and notes that the right rule sizes C against device memory; here C is the smallest power
-# of two covering max_steps, at most REV_C_MAX, halved while the scratch of every resident thread exceeds
-# REV_BUDGET_FRACTION of the free device memory.
-REV_C_MAX = 1024
-REV_BUDGET_FRACTION = 0.25
+# size (16 for small steps, a 64 KiB budget per thread) and notes that the right rule sizes C against device memory;
+# here, with HBM to spare: C = max_steps when every resident thread's head of max_steps + 1 states fits in
+# REV_BUDGET_FRACTION of the free device memory (no item then needs a checkpoint pass or a refill: the replay is
+# one forward evaluation and one VJP per step), else the largest power of two up to REV_C_POW2_MAX whose 3C + 1
+# states per thread fit.
+REV_BUDGET_FRACTION = 0.2
+REV_C_MIN = 16
+REV_C_POW2_MAX = 4096      # (the checkpointed fallback: beyond this C the replay's refill work is < 2% of K)
 
 
 _PLANS = {}
@@ -235,22 +238,31 @@ def replay_plan(p, max_steps, rev_checkpoints=None, device=None):
     return _PLANS[key]
 
 
+def replay_scratch_states(C, max_steps):
+    """compact states per thread of the replay scratch: the head alone when C >= max_steps, else head + checkpoints +
+    tape (the replay kernel's layout)"""
+    return C + 1 if C >= max_steps else 3 * C + 1
+
+
 def _replay_plan(p, max_steps, rev_checkpoints, device):
     kid, _ = _lib.kernel_id(p.kernel)
     info = _lib.kernel_info(kid)
     threads = info["sms"] * info["blocks_per_sm"] * info["block"]
-    per = lambda C: (3 * C + 1) * p.replay_state_bytes
+    M = int(max_steps)
+    per = lambda C: replay_scratch_states(C, M) * p.replay_state_bytes
     if rev_checkpoints is not None:
         C = int(rev_checkpoints)
         if C < 1:
             raise ValueError("tallymap_b200: rev_checkpoints must be >= 1")
     else:
-        C = 1
-        while C < min(int(max_steps), REV_C_MAX):
-            C *= 2
         free, _ = torch.cuda.mem_get_info(device)
-        while C > 16 and threads * per(C) > REV_BUDGET_FRACTION * free:
-            C //= 2
+        budget = REV_BUDGET_FRACTION * free
+        if M <= 2 ** 30 and threads * per(M) <= budget:
+            C = max(M, 1)
+        else:
+            C = REV_C_MIN
+            while C * 2 < M and C * 2 <= REV_C_POW2_MAX and threads * per(C * 2) <= budget:
+                C *= 2
     return C, threads, threads * per(C)
 
 
@@ -441,12 +453,12 @@ def _consts(vals, dev):
     return t
 
 
-def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None):
-    """result buffers for N items (an adjoint's replay scratch as planned on `device` unless given; a spawning
-    program's ring of `queue` slots; a recording program's `record` slots)."""
+def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None, max_steps=None):
+    """result buffers for N items (an adjoint's replay scratch as planned on `device` for `max_steps` unless given; a
+    spawning program's ring of `queue` slots; a recording program's `record` slots)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     if replay_bytes is None and p.replay_state_bytes:
-        replay_bytes = replay_plan(p, 2 ** 31 - 1, None, device)[2]
+        replay_bytes = replay_plan(p, max_steps or 2 ** 31 - 1, None, device)[2]
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
     R = record_capacity(N, record, device) if p.record_bytes else 0
     layout, _ = p.result_layout(N, replay_bytes or 0, Q, R)

@@ -131,14 +131,15 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
 //
 // B200 layout: the head, checkpoint and tape buffers (3C + 1 compact states per resident thread) live in a global
 // scratch buffer, contiguous per thread, so a lane's consecutive stores and loads fill and drain whole sectors; C is
-// a launch constant sized by the host from device memory (up to 1024: an item of K <= C steps is counted and swept
-// with no replay).  A lane in SWEEP applies up to V step VJPs per iteration (a VJP is a few instructions against a
+// a launch constant sized by the host from device memory: C >= max_steps when the heads of every resident thread fit
+// (then the scratch is the head alone, C + 1 states per thread, and every item is counted and swept with no replay:
+// one forward evaluation per step), else as large as the memory budget allows.  A lane in SWEEP applies up to V step VJPs per iteration (a VJP is a few instructions against a
 // forward step's two threefry2x32), so lanes sweeping and lanes stepping share the warp's iterations.
 //
 // ITEM additions for this kernel: Stored (the compact state: the carries a step reads that are not the step index),
 // store(State) -> Stored, restore(Ctx, Stored, i64 step) -> State, fwd(Ctx, State&) (one step, no emits),
 // vjp(Ctx, const State& at, Adj&) (the step VJP at the state before the step); kReplay (the scratch buffer) and the
-// launch constants kConstC (C) and kConstThreads (threads the scratch holds).
+// launch constants kConstM (max_steps), kConstC (C) and kConstThreads (threads the scratch holds).
 template <class I, int V>
 __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -161,7 +162,11 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   // takes no items: the others claim them; the error word records it (bit 1)
   const bool have = gtid < cap && C >= 1;
   if (!have) atomicOr(&ctl[kCtlError], 2u);
-  S* const head = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * (3 * (i64)C + 1);
+  // C >= max_steps: every item fits the head (K <= C, one segment, no checkpoints or tape), so a thread's scratch is
+  // the head alone
+  const bool head_only = C >= __ldg(&consts[I::kConstM]);
+  const i64 stride = head_only ? (i64)C + 1 : 3 * (i64)C + 1;
+  S* const head = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * stride;
   S* const ck = head + C + 1;
   S* const tape = ck + C;
 
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
         item = ticket_item(order, t);
         init = I::start(cx, item);
         x = init;
-        ck[0] = I::store(init);
+        if (!head_only) ck[0] = I::store(init);   // (read when a one-segment item refills: C < K)
         k = 0;
         I::adj_start(cx, adj);
         phase = COUNT;
