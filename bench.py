@@ -1,9 +1,12 @@
 #!/usr/bin/env python
 """Benchmark of the tallymap B200 backend on BASELINE config 2: the 1-D random walk, N = 4,194,304 items per GPU.
 
-One STEP = the forward launch plus the reverse-mode gradient launch (w.r.t. the broadcast `drift`) over the step's
-items: "Mitems/s fwd & grad"; the gradient's threads claim items longest first by the forward's trip counts (a
-device argsort inside the step).  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
+One STEP = the forward outputs plus the reverse-mode gradient (w.r.t. the broadcast `drift`, cotangent ones on the
+hist tally) over the step's items: "Mitems/s fwd & grad".  The step is timed as ONE fused value-and-grad launch
+(the replay whose count pass is the forward, what value_and_grad runs) where the item has one, else (--unfused, or
+items without one) as a forward launch then the replay launch, whose threads claim items longest first by the
+forward's trip counts (a device argsort inside the step); the separate forward and gradient times are reported too
+(fwd_ms, grad_ms).  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
 second) are synthetic, made with jax.random's algorithm on the host (tallymap_b200.prng).  Weak scaling: each rank
 runs its own 4,194,304 items (a contiguous slice of the global item set) and the partial tallies are combined with
 one NCCL collective step (all_reduce of the f32 / i32 tallies, all_gather + on-device combine of the exact gradient
@@ -114,6 +117,9 @@ def configs(B):
                   0, 0, 1048576,
                   "branching shower (BASELINE config 5): forward + tree-adjoint grad w.r.t. X0 (items = roots)"),
     }
+
+
+FAM = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz", "sh": "shower"}
 
 
 def replay_micro_steps(K, C):
@@ -261,6 +267,7 @@ def main():
     ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1", "od", "sh"])
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--unfused", action="store_true", help="time the step as a forward and a replay launch")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -320,18 +327,36 @@ def main():
                                    go[gnames.index("stats")])
         return out
 
+    # the fused value-and-grad launch (what value_and_grad runs for cotangents given up front), when the item has one
+    fused = None if (tree or args.unfused) else tm.FAMILIES[FAM[cfg.name]].fused.get((0,) if len(cfg.bc) == 1
+                                                                                       else tuple(range(len(cfg.bc))))
+    vo = None if fused is None else B.alloc_results(fused, N, dev, max_steps=cfg.max_steps)
+    vnames = None if fused is None else [n for n, _, _, _ in fused.result_layout(N)[0]]
+
+    def vg():
+        out = B.run(fused, pi, bc + ct, consts=(cfg.max_steps,), out=vo)
+        if world > 1:
+            parallel.all_reduce_sums(out[:ntal] + [out[ntal + 1]])
+            parallel.combine_exact(vo[vnames.index(fused.tallies[-1].name + ".exact")], nb, g_all,
+                                   vo[vnames.index("stats")])
+        return out
+
     for _ in range(args.warmup):
         fwd()
         grad()
+        if fused is not None:
+            vg()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = Clocks(getattr(torch.cuda.get_device_properties(dev), "pci_bus_id", None))
     clocks.start()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evf = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    # (1) the step as two launches: the forward, then the gradient (replay) alone -- the reference's two numbers
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record(stream)
@@ -339,20 +364,29 @@ def main():
         ev[i][1].record(stream)
         grad()
         ev[i][2].record(stream)
+    # (2) the step as one fused value-and-grad launch
+    if fused is not None:
+        for i in range(args.steps):
+            flush.zero_()
+            evf[i][0].record(stream)
+            vg()
+            evf[i][1].record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     f_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
     g_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
-    t = torch.tensor([f_ms + g_ms, f_ms, g_ms], dtype=torch.float64, device=dev)
+    v_ms = sum(e[0].elapsed_time(e[1]) for e in evf) if fused is not None else 0.0
+    t = torch.tensor([f_ms + g_ms, f_ms, g_ms, v_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    tot_ms, f_ms, g_ms = (float(v) / args.steps for v in t.tolist())
+    sep_ms, f_ms, g_ms, v_ms = (float(v) / args.steps for v in t.tolist())
+    tot_ms = v_ms if fused is not None else sep_ms
     value = N * world / (tot_ms / 1e3) / 1e6
 
     # ---- e2e: the public API from pinned host inputs, H2D + both launches + result read-back timed
-    fam = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz", "sh": "shower"}[cfg.name]
+    fam = FAM[cfg.name]
     F = tm.FAMILIES[fam]
     f = tm.vmap(fam, outputs={t.name: tm.Sum(t.dims(N), t.dtype) for t in F.fwd.tallies}, in_axes=F.in_axes,
                 max_steps=cfg.max_steps)
@@ -411,6 +445,12 @@ def main():
     torch.cuda.synchronize()
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
     dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
+    if fused is not None:
+        # the fused launch: the replay's schedule, its count pass being the forward (cfg.tf threefry2x32 per
+        # evaluation), plus the step VJPs
+        C_vg = B.replay_plan(fused, cfg.max_steps, None, dev)[0]
+        tf_vg = cfg.tf * (replay_micro_steps(kk, C_vg) - steps_total) + cfg.tf_vjp * steps_total
+        dom = (fused.kernel, tf_vg, v_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
     tr = TRAFFIC.get(dom[0])
     traffic = None if tr is None else int(round(tr[0] * N))
@@ -430,7 +470,7 @@ def main():
         cpu = {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port",
                "sample": f"oracle port (the reference CPU kernel target's model: f32 tallies, libm): fwd + grad of "
                          f"the first {n} items, {dt:.1f} s on {nth} OpenMP threads"}
-    info = _lib.kernel_info(_lib.kernel_id(cfg.grad.kernel)[0])
+    info = _lib.kernel_info(_lib.kernel_id((fused or cfg.grad).kernel)[0])
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
@@ -439,7 +479,10 @@ def main():
                    "max_steps": cfg.max_steps, "rev_checkpoints": C_used,
                    "parallelism": f"items sharded over {world} GPU(s)",
                    "l2": "flushed between timed steps (256 MiB write)"},
-        "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3),
+        "step": ("one fused value-and-grad launch (" + fused.kernel + ")") if fused is not None else
+                "a forward launch, then the gradient launch(es)",
+        "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3), "separate_ms": round(sep_ms, 3),
+        "fused_ms": round(v_ms, 3) if fused is not None else None,
         "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),
         "grad_mitems_s": round(N * world / (g_ms / 1e3) / 1e6, 3),
         "mean_trip_count": round(steps_total / N, 2),
@@ -449,7 +492,8 @@ def main():
            if tree else {}),
         "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
                 "h2d_bytes_per_step": int(sum(h.nbytes for h in host)), "d2h_bytes_per_step": int(d2h[0])},
-        "gpu_launches": args.steps * ((1 + tree_info["kernels"]) if tree else (2 + (1 if world > 1 else 0))),
+        "gpu_launches": args.steps * ((1 + tree_info["kernels"]) if tree else
+                                      ((1 if fused is not None else 2) + (1 if world > 1 else 0))),
         "roofline": roofline,
         "clocks": clk,
         "kernel_resources": info,

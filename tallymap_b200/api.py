@@ -48,11 +48,12 @@ class Family:
     grads: dict          # tuple of broadcast operand indices -> the adjoint program giving their cotangents
     in_axes: tuple
     default_max_steps: int
+    fused: dict = dataclasses.field(default_factory=dict)   # the same keys -> value-and-grad program (one launch)
 
 
 FAMILIES = {
-    "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100),
-    "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000),
+    "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100, {(0,): B.Q1_VG}),
+    "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000, {(0,): B.RW_VG}),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
@@ -108,11 +109,15 @@ class Mapped:
         outs = _poison(tallies, n_tr > 0)
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
-    def value_and_grad(self, *args, wrt, cotangents):
-        """(Result, gradient) of one forward and one replay launch, with the inputs moved to the device once.  The
-        replay claims items longest first by the forward's trip counts (an LPT schedule: the replay of an item costs
-        a known function of its trip count), which balances the threads' work and keeps a warp's lanes in the same
-        replay phase; it changes no result (the cotangent tally is exact, per-item results are indexed by item)."""
+    def value_and_grad(self, *args, wrt, cotangents, fused=True):
+        """(Result, gradient of <cotangents, outputs>) with the inputs moved to the device once.  The cotangents are
+        given up front, so where the item has a fused program this is ONE launch: the replay's count pass is the
+        forward pass, emitting the forward's tallies while it stores the states the step VJPs then read (bitwise the
+        separate forward and replay; tests/test_fused_gpu.py).  Otherwise (or fused=False) one forward and one
+        replay launch; the replay claims items longest first by the forward's trip counts (an LPT schedule: the
+        replay of an item costs a known function of its trip count), which balances the threads' work and keeps a
+        warp's lanes in the same replay phase; it changes no result (the cotangent tally is exact, per-item results
+        are indexed by item)."""
         dev = torch.device("cuda", torch.cuda.current_device())
         moved = []
         for a, ax in zip(args, self.fam.in_axes):
@@ -121,6 +126,10 @@ class Mapped:
                 moved.append(t.to(dev, non_blocking=True))
             else:
                 moved.append(a)
+        if fused:
+            r = self._fused(moved, wrt, cotangents)
+            if r is not None:
+                return r
         res = self(*moved)
         order = None
         if "tree" not in self.fam.grads and isinstance(res.per_item, torch.Tensor) and \
@@ -157,6 +166,42 @@ class Mapped:
         ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
         return ct.reshape(()) if isinstance(wrt, int) else ct
 
+
+    def _cotangents(self, n, cotangents):
+        return [torch.zeros(t.dims(n), dtype=t.dtype) if cotangents.get(t.name) is None else cotangents[t.name]
+                for t in self.fam.fwd.tallies]
+
+    def _fused(self, args, wrt, cotangents):
+        """(Result, gradient) from the family's value-and-grad program, or None when it has none for `wrt`"""
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if any(self.fam.in_axes[w] is not None for w in idx):
+            return None
+        bpos = tuple(sum(1 for ax in self.fam.in_axes[:w] if ax is None) for w in idx)
+        prog, sel = None, None
+        for key, g in self.fam.fused.items():
+            if all(b in key for b in bpos):
+                prog, sel = g, [key.index(b) for b in bpos]
+                break
+        if prog is None:
+            return None
+        pi, bc = self._split(args)
+        n = int(pi[0].shape[0]) if pi else 0
+        out = B.run(prog, pi, list(bc) + self._cotangents(n, cotangents), consts=(self.max_steps,))
+        p = self.fam.fwd
+        nt = len(p.tallies)
+        tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
+        ct = out[nt].reshape(-1)[sel]
+        stats_raw = out[nt + 1]
+        ys = out[nt + 2:]
+        trunc = ys[p.trunc].bool()
+        per = [y for i, y in enumerate(ys) if i != p.trunc]
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {nm: stats_raw[i] for i, nm in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        bad = n_tr > 0
+        res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        ct = torch.where(bad, torch.full_like(ct, float("nan")), ct)
+        return res, (ct.reshape(()) if isinstance(wrt, int) else ct)
 
     def _tree_grad(self, args, idx, cotangents, wrt):
         """the gradient of a spawning item through its children (tallymap/_reverse_spawn.py:233-336): the recording

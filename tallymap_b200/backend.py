@@ -74,6 +74,8 @@ class ItemProgram:
     queue_leaf_bytes: int = 0       # a spawning program: bytes of one child's leaves in the ring
     record_bytes: int = 0           # a recording spawning program: bytes of one child's record (tree adjoint)
     buffers: int = 0                # nonzero: launched by its own driver with this many buffers (not by run())
+    vg_fallback: str = None         # a pipelined value-and-grad program: its kernel needs C >= max_steps (two heads
+                                    # per thread); with a smaller C the launch uses this fused replay kernel instead
 
     @property
     def n_args(self):
@@ -146,6 +148,15 @@ RW_GRAD = ItemProgram("rw_grad", "rw_grad", pi=(Operand("x", (), _F32), KEY),
                       tallies=(TSpec("ct_drift", (1,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=4)
 
+# value and gradient in one launch (FusedVG: the replay's count pass is the forward pass, emitting its tallies), for
+# cotangents given up front: the forward's tallies, then the gradient's exact tally; the forward's per-item results
+Q1_VG = ItemProgram("q1_vg", "q1_vg", pi=Q1_GRAD.pi, bc=Q1_GRAD.bc, consts=Q1_GRAD.consts,
+                    tallies=Q1_FWD.tallies + Q1_GRAD.tallies, ys=Q1_FWD.ys, trunc=1, replay_state_bytes=4,
+                    vg_fallback="q1_vg_replay")
+RW_VG = ItemProgram("rw_vg", "rw_vg", pi=RW_GRAD.pi, bc=RW_GRAD.bc, consts=RW_GRAD.consts,
+                    tallies=RW_FWD.tallies + RW_GRAD.tallies, ys=RW_FWD.ys, trunc=1, replay_state_bytes=4,
+                    vg_fallback="rw_vg_replay")
+
 # BASELINE config 3, the photon slab (csrc/items_photon.cuh)
 PH_FWD = ItemProgram("ph_fwd", "ph_fwd", pi=(KEY,), bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32)),
                      consts=("max_steps",), tallies=(TSpec("dep", (64, 64, 64), f64=True),),
@@ -188,8 +199,8 @@ SH_GRAD = ItemProgram("sh_grad", "sh_grad", pi=SH_PI,
                       consts=("max_steps", "rev_checkpoints", "replay_threads", "roots", "record"),
                       tallies=(TSpec("ct_X0", (1,), exact=True),), ys=(), replay_state_bytes=4, buffers=18)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, RW_FWD, RW_GRAD, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD, SH_FWD, SH_REC,
-                                SH_GRAD)}
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, RW_FWD, RW_GRAD, RW_VG, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD,
+                                SH_FWD, SH_REC, SH_GRAD)}
 
 
 # -------------------------------------------------------------------------------------------------- run
@@ -238,10 +249,12 @@ def replay_plan(p, max_steps, rev_checkpoints=None, device=None):
     return _PLANS[key]
 
 
-def replay_scratch_states(C, max_steps):
-    """compact states per thread of the replay scratch: the head alone when C >= max_steps, else head + checkpoints +
-    tape (the replay kernel's layout)"""
-    return C + 1 if C >= max_steps else 3 * C + 1
+def replay_scratch_states(C, max_steps, pipelined=False):
+    """compact states per thread of the replay scratch: the head alone when C >= max_steps (two heads for a pipelined
+    value-and-grad kernel), else head + checkpoints + tape (the replay kernel's layout)"""
+    if C >= max_steps:
+        return 2 * (C + 1) if pipelined else C + 1
+    return 3 * C + 1
 
 
 def _replay_plan(p, max_steps, rev_checkpoints, device):
@@ -249,7 +262,7 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
     info = _lib.kernel_info(kid)
     threads = info["sms"] * info["blocks_per_sm"] * info["block"]
     M = int(max_steps)
-    per = lambda C: replay_scratch_states(C, M) * p.replay_state_bytes
+    per = lambda C: replay_scratch_states(C, M, p.vg_fallback is not None) * p.replay_state_bytes
     if rev_checkpoints is not None:
         C = int(rev_checkpoints)
         if C < 1:
@@ -315,17 +328,21 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     res = out if out is not None else alloc_results(p, N, dev, replay_bytes, Q, R)
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
-    kid, nbuf = _lib.kernel_id(p.kernel)
+    kernel = p.kernel
+    if p.vg_fallback is not None and known["rev_checkpoints"] < known["max_steps"]:
+        kernel = p.vg_fallback          # (items may outgrow the head: the fused replay's checkpointed schedule)
+    kid, nbuf = _lib.kernel_id(kernel)
     ptrs = [0 if t is None else t.data_ptr() for t in args] + [t.data_ptr() for t in res]
     if len(ptrs) != nbuf:
-        raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {p.kernel} takes {nbuf}")
+        raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {kernel} takes {nbuf}")
     st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
     flags = (4 if p.spawns else 0) | 8
     _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=flags)
     names = [n for n, _, _, _ in layout]
     tallies = [res[names.index(t.name)] for t in p.tallies]
     ys = res[n_zero:n_zero + len(p.ys)]
-    run.last = dict(ctl=res[names.index("ctl")], args=args, consts=consts, results=dict(zip(names, res)))
+    run.last = dict(ctl=res[names.index("ctl")], args=args, consts=consts, results=dict(zip(names, res)),
+                    kernel=kernel)
     return tallies + [res[names.index("stats")]] + list(ys)
 
 

@@ -301,4 +301,36 @@ struct RWGrad : RWCommon {
   }
 };
 
+// ================================================================================================= value and grad
+// The fused programs (FusedVG, tm_runtime.cuh): the forward's outputs and the gradient of <ct, outputs> in one launch.
+//   q1_vg    x0, keys, theta, ct_hist, consts, order | hist f32[16], g_theta f32[1], exact u64[6], ctl, stats |
+//            k i32[N], trunc u8[N], replay scratch
+//   rw_vg    x0, keys, drift, ct_hist, ct_side, consts, order | hist f32[256], side f32[2], g_drift f32[1],
+//            exact u64[6], ctl, stats | k i32[N], trunc u8[N], replay scratch
+struct Q1VGMap {
+  enum { kNF = Q1Fwd::kNBuf, kNG = Q1Grad::kNBuf, kNBuf = 14 };
+  __host__ __device__ static constexpr int f(int i) {
+    constexpr int m[kNF] = {0, 1, 2, 4, 5, 6, 9, 10, 11, 12};
+    return m[i];
+  }
+  __host__ __device__ static constexpr int g(int i) {
+    constexpr int m[kNG] = {0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 12, 13};
+    return m[i];
+  }
+};
+typedef FusedVG<Q1Fwd, Q1Grad, Q1VGMap> Q1VG;
+
+struct RWVGMap {
+  enum { kNF = RWFwd::kNBuf, kNG = RWGrad::kNBuf, kNBuf = 16 };
+  __host__ __device__ static constexpr int f(int i) {
+    constexpr int m[kNF] = {0, 1, 2, 5, 6, 7, 8, 11, 12, 13, 14};
+    return m[i];
+  }
+  __host__ __device__ static constexpr int g(int i) {
+    constexpr int m[kNG] = {0, 1, 2, 3, 4, 5, 6, 9, 10, 11, 12, 14, 15};
+    return m[i];
+  }
+};
+typedef FusedVG<RWFwd, RWGrad, RWVGMap> RWVG;
+
 }  // namespace tmb

@@ -84,6 +84,17 @@ void add_spawn(const char* name) {
 }
 
 template <class I, int V>
+void add_vg(const char* name) {
+  Kernel k;
+  k.name = name;
+  k.fn = reinterpret_cast<const void*>(&tmb::vg_kernel<I, V>);
+  k.nbuf = I::kNBuf;
+  k.smem = I::kSmemBytes;
+  (*g_reg)[name_id(name)] = k;
+  g_names->push_back(name);
+}
+
+template <class I, int V>
 void add_replay(const char* name) {
   Kernel k;
   k.name = name;
@@ -104,6 +115,10 @@ void init_registry() {
   add_replay<tmb::Q1Grad, 4>("q1_grad");
   add_forward<tmb::RWFwd>("rw_fwd");
   add_replay<tmb::RWGrad, 4>("rw_grad");
+  add_vg<tmb::Q1VG, 4>("q1_vg");
+  add_vg<tmb::RWVG, 4>("rw_vg");
+  add_replay<tmb::Q1VG, 4>("q1_vg_replay");
+  add_replay<tmb::RWVG, 4>("rw_vg_replay");
   add_forward<tmb::PHFwd>("ph_fwd");
   add_replay<tmb::PHGrad, 1>("ph_grad");
   add_forward<tmb::ODFwd>("od_fwd");

@@ -28,6 +28,8 @@
 //                                      emits, per-item results (the replay's truncation flag)
 //   void adj_flush(const Ctx&, unsigned char* smem, int tid, int nth)  (private accumulators -> shared -> global)
 #pragma once
+#include <type_traits>
+
 #include "tm_device.cuh"
 
 namespace tmb {
@@ -118,6 +120,14 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
   finish_block<I>(cx, ctl);
 }
 
+// An ITEM with `static constexpr bool kFused = true` is a value-and-gradient program (FusedVG below): its replay's
+// count pass is the forward pass itself, emitting the forward tallies (fwd_emit) and writing the forward's per-item
+// results (fwd_finish), so one launch yields the outputs and their gradient for cotangents given up front.
+template <class T, class = void>
+struct fused_trait : std::false_type {};
+template <class T>
+struct fused_trait<T, std::void_t<decltype(T::kFused)>> : std::integral_constant<bool, T::kFused> {};
+
 // ------------------------------------------------------------------------------------------------ replay kernel
 // The reverse-mode program of an item with one top-level loop: the checkpointed loop of tallymap/_reverse.py:324-444
 // run as a per-lane state machine, one loop step per iteration (or up to V step VJPs).  Per item:
@@ -180,17 +190,20 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   bool first = false;
   // warp-uniform loop: a lane with no work left keeps iterating (idle) until its whole warp is done; after the
   // (divergent) bookkeeping the warp reconverges, so every lane that steps runs the step body in one pass
+  constexpr bool kFused = fused_trait<I>::value;
   for (;;) {
-    bool vjp = false, stop = phase < 0;
+    bool vjp = false, stop = phase < 0, counting = false;
     while (!stop) {   // bookkeeping until this lane has a step or step VJPs to evaluate
       if (phase == COUNT) {
         if (I::cond(cx, x)) {
           head[k < C ? k : C] = I::store(x);
           ++k;
+          counting = true;
           break;
         }
         K = k;
         fin = x;
+        if constexpr (kFused) I::fwd_finish(cx, fin, item);
         I::post_vjp(cx, fin, adj);
         m = (i64)K > (i64)C * C ? (K + C - 1) / C : C;
         ns = (K + m - 1) / m;
@@ -255,7 +268,13 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
     }
     if (!__any_sync(0xffffffffu, phase >= 0)) break;
     __syncwarp();
-    if (!stop && !vjp) I::fwd(cx, x);
+    if (!stop && !vjp) {
+      if constexpr (kFused) {
+        I::fwd_emit(cx, x, counting);   // the count pass emits the forward tallies; checkpoint and refill passes do not
+      } else {
+        I::fwd(cx, x);
+      }
+    }
     __syncwarp();
     if (vjp) {
       // up to V stored states, newest first: the loads issue together, then the VJPs run in order
@@ -273,5 +292,178 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   I::adj_flush(cx, smem, threadIdx.x, blockDim.x);
   finish_block<I>(cx, ctl);
 }
+
+// ------------------------------------------------------------------------------------------------ pipelined value and grad
+// vg_kernel<I, V>: a fused value-and-grad program (I::kFused) when every item fits the head (C >= max_steps).  In the
+// replay kernel a lane counts an item, then sweeps it, so at any iteration some lanes of a warp count and others
+// sweep and the warp pays for both paths.  Here each lane pipelines two items through two head buffers: it counts
+// item n (one forward step with emits per iteration, storing the states) while it sweeps item n - 1 (up to V step
+// VJPs per iteration, newest first) from the other buffer.  Every iteration then runs the forward step for (nearly)
+// every lane; a lane whose count ends before its previous sweep does waits, sweeping, until the sweep is done.  The
+// step VJPs of an item run in the replay's order on the same states, so the gradient is bitwise the replay's.
+// Scratch: 2 (C + 1) states per thread.  ITEM additions: handoff(Ctx& sweep, const Ctx& count) gives the sweeping
+// context an item's per-item context while keeping its own per-thread accumulators.
+template <class I, int V>
+__global__ void __launch_bounds__(TM_BLOCK) vg_kernel(const Params P, const i64 n_items) {
+  static_assert(fused_trait<I>::value, "vg_kernel runs fused value-and-grad programs");
+  extern __shared__ __align__(16) unsigned char smem[];
+  typename I::Ctx cx;
+  I::setup(cx, P, smem);
+  smem_zero(smem, I::kSmemBytes);
+  __syncthreads();
+  I::stage(P, smem);
+  __syncthreads();
+  u32* const ctl = static_cast<u32*>(P.p[I::kCtl]);
+  u64* const ctr = reinterpret_cast<u64*>(ctl + kCtlClaim);
+  const i32* const consts = static_cast<const i32*>(P.p[I::kConsts]);
+  const i32* const order = static_cast<const i32*>(P.p[I::kOrder]);
+  const i32 C = __ldg(&consts[I::kConstC]);
+  const i64 cap = __ldg(&consts[I::kConstThreads]);
+  const i64 gtid = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  typedef typename I::Stored S;
+  typedef typename I::State X;
+  // the host launches this kernel only with C >= max_steps; a thread beyond the planned scratch, or a launch that
+  // breaks that rule, takes no items and sets the error word (bit 1)
+  const bool have = gtid < cap && C >= 1 && C >= __ldg(&consts[I::kConstM]);
+  if (!have) atomicOr(&ctl[kCtlError], 2u);
+  S* const buf = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * 2 * ((i64)C + 1);
+  typename I::Ctx cs = cx;          // the sweeping item's context
+  X x, xinit, sinit, sfin;
+  typename I::Adj adj;
+  i64 item = 0, sitem = 0;
+  i32 k = 0, si = -1;               // si >= 0: the sweep's next state index
+  int cb = 0, sb = 1;               // the buffers of the counting and the sweeping item
+  bool counting = false, alive = have;
+  for (;;) {
+    bool c_ok = counting && I::cond(cx, x);
+    if (counting && !c_ok && si < 0) {
+      // the count pass ended: the forward's post-loop code, then the item moves to the sweep slot
+      I::fwd_finish(cx, x, item);
+      I::handoff(cs, cx);
+      sinit = xinit;
+      sfin = x;
+      sitem = item;
+      sb = cb;
+      cb ^= 1;
+      I::adj_start(cs, adj);
+      I::post_vjp(cs, sfin, adj);
+      si = k - 1;
+      if (si < 0) I::adj_finish(cs, sinit, sfin, adj, sitem);
+      counting = false;
+    }
+    if (alive && !counting) {
+      const u64 t = claim_item(ctr);
+      if (t >= (u64)n_items) {
+        alive = false;
+      } else {
+        item = ticket_item(order, t);
+        x = I::start(cx, item);
+        xinit = x;
+        k = 0;
+        counting = true;
+        c_ok = I::cond(cx, x);
+      }
+    }
+    if (!__any_sync(0xffffffffu, counting || si >= 0)) break;
+    __syncwarp();
+    if (c_ok) {
+      buf[cb * ((i64)C + 1) + k] = I::store(x);
+      ++k;
+      I::fwd_emit(cx, x, true);
+    }
+    __syncwarp();
+    if (si >= 0) {
+      const S* const src = buf + sb * ((i64)C + 1);
+      S st[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) st[v] = src[si - v >= 0 ? si - v : 0];
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        if (si - v >= 0) I::vjp(cs, I::restore(cs, st[v], si - v), adj);
+      si -= V;
+      if (si < 0) I::adj_finish(cs, sinit, sfin, adj, sitem);
+    }
+  }
+  __syncthreads();
+  I::handoff(cs, cx);   // one context for the flush: the counting context's, with the sweeping one's accumulators
+  I::adj_flush(cs, smem, threadIdx.x, blockDim.x);
+  finish_block<I>(cs, ctl);
+}
+
+// ------------------------------------------------------------------------------------------------ value and grad
+// FusedVG<F, G, Map>: forward item F and its adjoint G as one replay program.  The launch's buffers are G's, with F's
+// result buffers that G lacks (its tallies and per-item results) inserted where the host's layout puts them; Map
+// gives, for each of F's and G's buffer indices, the fused index (Map::f(i), Map::g(i); shared buffers -- inputs,
+// constants, claim order, control words, stats, the truncation flags -- map to one index) and Map::kNF, kNG, kNBuf
+// the buffer counts.  G's constants start with max_steps, as F's.  Shared memory: G's block, then F's (16-byte
+// aligned).
+template <class F, class G, class Map>
+struct FusedVG {
+  static constexpr bool kFused = true;
+  static constexpr int kGSmem = (G::kSmemBytes + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kGSmem + F::kSmemBytes;
+  enum { kConsts = Map::g(G::kConsts), kOrder = Map::g(G::kOrder), kCtl = Map::g(G::kCtl),
+         kReplay = Map::g(G::kReplay), kNBuf = Map::kNBuf };
+  enum { kConstM = G::kConstM, kConstC = G::kConstC, kConstThreads = G::kConstThreads };
+  typedef typename G::State State;
+  typedef typename G::Adj Adj;
+  typedef typename G::Stored Stored;
+  struct Ctx {
+    typename G::Ctx g;
+    typename F::Ctx f;
+  };
+  __device__ __forceinline__ static Params remap_g(const Params& P) {
+    Params Q;
+#pragma unroll
+    for (int i = 0; i < Map::kNG; ++i) Q.p[i] = P.p[Map::g(i)];
+    return Q;
+  }
+  __device__ __forceinline__ static Params remap_f(const Params& P) {
+    Params Q;
+#pragma unroll
+    for (int i = 0; i < Map::kNF; ++i) Q.p[i] = P.p[Map::f(i)];
+    return Q;
+  }
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    G::setup(c.g, remap_g(P), smem);
+    F::setup(c.f, remap_f(P), smem + kGSmem);
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    G::stage(remap_g(P), smem);
+    F::stage(remap_f(P), smem + kGSmem);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    F::start(c.f, item);
+    return G::start(c.g, item);
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return G::cond(c.g, s); }
+  __device__ __forceinline__ static void fwd_emit(const Ctx& c, State& s, bool emit) {
+    if (emit) F::step(c.f, s);
+    else G::fwd(c.g, s);
+  }
+  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) { G::fwd(c.g, s); }
+  __device__ static void fwd_finish(const Ctx& c, const State& fin, i64 item) { F::finish(c.f, fin, item); }
+  __device__ __forceinline__ static void handoff(Ctx& sweep, const Ctx& count) {
+    const auto pv = sweep.g.pv;      // the thread's exact cotangent words stay with the sweeping context
+    sweep = count;
+    sweep.g.pv = pv;
+  }
+  __device__ static void adj_start(const Ctx& c, Adj& a) { G::adj_start(c.g, a); }
+  __device__ __forceinline__ static Stored store(const State& s) { return G::store(s); }
+  __device__ __forceinline__ static State restore(const Ctx& c, Stored v, i64 step) { return G::restore(c.g, v, step); }
+  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) { G::vjp(c.g, at, a); }
+  __device__ static void post_vjp(const Ctx& c, const State& fin, Adj& a) { G::post_vjp(c.g, fin, a); }
+  __device__ static void adj_finish(const Ctx& c, const State& init, const State& fin, Adj& a, i64 item) {
+    G::adj_finish(c.g, init, fin, a, item);
+  }
+  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int nth) {
+    G::adj_flush(c.g, smem, tid, nth);
+    F::flush(c.f, smem + kGSmem, tid, nth);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int nth) {
+    G::epilogue(c.g, tid, nth);
+    F::epilogue(c.f, tid, nth);
+  }
+};
 
 }  // namespace tmb
