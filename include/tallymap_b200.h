@@ -52,6 +52,14 @@ int tm_kernel_name(int32_t i, const char** name);
 int tm_register(int64_t id, const void* image, size_t n, const char* note, int32_t n_buffers, int32_t smem_bytes,
                 int32_t block);
 
+/* Compile a lowered item program for sm_100a with NVRTC (libnvrtc.so.12, loaded on first use) and register it as
+ * tm_register does: `source` is CUDA C++ that includes the runtime headers found in `include_dir` and defines
+ * `extern "C" __global__ void tm_main(tmb::Params, long long)`.  Compiled with -arch=sm_100a -std=c++17 --fmad=false
+ * -lineinfo.  On a compile error returns TM_EINVAL with the NVRTC log in tm_last_error().
+ * Replaces: compile_cubin + tallymap_register (backends/kernel/compile.py:160-173, shim.cc:134-142). */
+int tm_compile_register(int64_t id, const char* source, const char* include_dir, const char* note,
+                        int32_t n_buffers, int32_t smem_bytes, int32_t block);
+
 /* Resources of a kernel on the current device: out[7] = registers per thread, local bytes per thread, static
  * shared bytes per block, resident blocks per SM, SMs, max resident threads per SM, block size.
  * Replaces: tallymap_kernel_info (backends/kernel/shim.cc:147-155). */

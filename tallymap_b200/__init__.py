@@ -2,17 +2,18 @@
 
 Layers (top down):
   api.vmap / Result      the tallymap result contract (poisoning, stats) over lowered item programs
+  lang, trace, lower     Python item functions: traced to a scalar IR, lowered to CUDA, compiled at run time (NVRTC)
   backend.run            the kernel-backend driver, the counterpart of tallymap/backends/kernel/__init__.py:135 run
   _lib                   ctypes binding of libtm_b200.so, the C ABI of include/tallymap_b200.h
   csrc/                  the persistent-thread runtime and item programs, CUDA for sm_100a
   prng                   jax.random key arithmetic on the host (numpy), for inputs made without JAX
   parallel               items sharded over GPUs, tallies combined with NCCL
 """
-from . import prng
+from . import lang, prng
 from ._lib import TallymapError, build
 from .api import FAMILIES, Result, Sum, vmap
 from .backend import PROGRAMS, STATS, ItemProgram, TSpec, run
 
 __version__ = "0.1.0"
-__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "Result", "Sum", "TSpec", "TallymapError", "build", "prng",
-           "run", "vmap"]
+__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "Result", "Sum", "TSpec", "TallymapError", "build", "lang",
+           "prng", "run", "vmap"]

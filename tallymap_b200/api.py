@@ -224,6 +224,122 @@ def longest_first(k):
     return torch.argsort(k, descending=True, stable=True).to(torch.int32)
 
 
+class MappedFn:
+    """tallymap.vmap over a Python item function: traced (tallymap_b200.trace) on its first call with a given
+    operand signature, lowered to CUDA and compiled for sm_100a at run time (tallymap_b200.lower, NVRTC); the reverse
+    programs are lowered and compiled on the first gradient request for each set of differentiated operands."""
+
+    def __init__(self, fn, outputs, in_axes, max_steps):
+        self.fn = fn
+        self.outputs = {}
+        for name, o in outputs.items():
+            if o.dtype not in (torch.float32, torch.int32):
+                raise TypeError(f"tallymap_b200: output {name!r}: Sum of float32 or int32")
+            self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32")
+        self.in_axes = tuple(in_axes)
+        if any(ax not in (0, None) for ax in self.in_axes):
+            raise ValueError("tallymap_b200: in_axes entries are 0 (per item) or None (broadcast)")
+        self.max_steps = int(2 ** 31 - 1 if max_steps is None else max_steps)
+        if self.max_steps < 1:
+            raise ValueError("tallymap_b200: max_steps must be >= 1")
+        self._lowered = {}
+        self.last_lowered = None
+
+    @staticmethod
+    def _spec(a, per_item):
+        t = a if isinstance(a, torch.Tensor) else torch.from_numpy(B._host(a))
+        dt = {torch.float32: "f32", torch.int32: "i32", torch.uint32: "u32"}.get(t.dtype)
+        if dt is None:
+            raise TypeError(f"tallymap_b200: operand dtype {t.dtype} (float32, int32 or uint32 key data)")
+        shape = tuple(t.shape[1:]) if per_item else tuple(t.shape)
+        if shape == ():
+            return dt if dt != "u32" else "i32"
+        if per_item and shape == (2,) and dt in ("i32", "u32"):
+            return "key"                      # uint32[N, 2] key data (int32 bits on torch)
+        if per_item and len(shape) == 1 and dt == "f32":
+            return ("f32", shape[0])
+        raise TypeError(f"tallymap_b200: operand of per-item shape {shape} and dtype {dt} is not lowered")
+
+    def lowered(self, args):
+        from . import lower
+        if len(args) != len(self.in_axes):
+            raise TypeError(f"tallymap_b200: the item takes {len(self.in_axes)} arguments, got {len(args)}")
+        pis = [self._spec(a, True) for a, ax in zip(args, self.in_axes) if ax == 0]
+        bcs = [self._spec(a, False) for a, ax in zip(args, self.in_axes) if ax is None]
+        key = (tuple(pis), tuple(bcs))
+        if key not in self._lowered:
+            order = [ax for ax in self.in_axes]
+            # the item's arguments in their declared order; the lowering wants per-item first
+            perm = [i for i, ax in enumerate(order) if ax == 0] + [i for i, ax in enumerate(order) if ax is None]
+
+            def item(t, *xs):
+                args_ = [None] * len(xs)
+                for pos, x in zip(perm, xs):
+                    args_[pos] = x
+                return self.fn(t, *args_)
+            item.__name__ = getattr(self.fn, "__name__", "item")
+            self._lowered[key] = lower.Lowered(item, pis + bcs, len(pis), self.outputs)
+        self.last_lowered = self._lowered[key]
+        return self._lowered[key]
+
+    def _split(self, args):
+        pi = [a for a, ax in zip(args, self.in_axes) if ax == 0]
+        bc = [a for a, ax in zip(args, self.in_axes) if ax is None]
+        return pi, bc
+
+    def __call__(self, *args):
+        L = self.lowered(args)
+        pi, bc = self._split(args)
+        p = L.fwd
+        out = B.run(p, pi, bc, consts=(self.max_steps,))
+        nt = len(p.tallies)
+        tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
+        stats_raw = out[nt]
+        ys = out[nt + 1:]
+        trunc = ys[p.trunc].bool()
+        per = [y for i, y in enumerate(ys) if i != p.trunc]
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        return Result(_poison(tallies, n_tr > 0), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+
+    def grad(self, *args, wrt, cotangents, order=None):
+        """d <cotangents, outputs> / d args[wrt] for float32 broadcast operand(s) `wrt`: ONE replay launch of the
+        generated adjoint.  -> a scalar for one index, a vector for a tuple; NaN when an item's replay hit
+        max_steps."""
+        L = self.lowered(args)
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if any(self.in_axes[w] is not None for w in idx):
+            raise ValueError("tallymap_b200: grad with respect to a per-item operand is not lowered")
+        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
+        prog = L.grad_program(bpos)
+        pi, bc = self._split(args)
+        n = int((pi[0] if isinstance(pi[0], torch.Tensor) else B._host(pi[0])).shape[0]) if pi else 0
+        cts = []
+        for name, (shape, dt) in self.outputs.items():
+            if dt != "f32":
+                continue
+            c = cotangents.get(name)
+            cts.append(torch.zeros(shape, dtype=torch.float32) if c is None else c)
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
+        ct = out[0].reshape(-1)
+        trunc = out[2]
+        ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
+        return ct.reshape(()) if isinstance(wrt, int) else ct
+
+    def value_and_grad(self, *args, wrt, cotangents):
+        """(Result, gradient): the forward launch and the generated replay launch"""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        moved = [(a if isinstance(a, torch.Tensor) else torch.from_numpy(B._host(a))).to(dev, non_blocking=True)
+                 if ax == 0 else a for a, ax in zip(args, self.in_axes)]
+        return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
+
+
 def vmap(item, outputs, in_axes, max_steps=None):
+    """tallymap.vmap: `item` is a Python function written against tallymap_b200.lang (traced, lowered and compiled
+    on first call) or the name of a built-in lowered family ("quickstart", "walk1d", "photon", "lorenz",
+    "shower")."""
+    if callable(item) and not isinstance(item, Family):
+        return MappedFn(item, outputs, in_axes, max_steps)
     fam = FAMILIES[item] if isinstance(item, str) else item
     return Mapped(fam, outputs, in_axes, max_steps)

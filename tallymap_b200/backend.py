@@ -204,6 +204,18 @@ PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, RW_FWD, RW_GRAD, RW_VG, 
 
 
 # -------------------------------------------------------------------------------------------------- run
+COMPILED = {}      # kernel id of a program compiled at run time (tallymap_b200.lower) -> its buffer count
+
+
+def kernel_ref(kernel):
+    """(kernel id, buffer count) of a built-in kernel name or of a run-time compiled kernel id"""
+    if isinstance(kernel, int):
+        if kernel not in COMPILED:
+            raise _lib.TallymapError(f"tallymap_b200: kernel id {kernel} was not compiled in this process")
+        return kernel, COMPILED[kernel]
+    return _lib.kernel_id(kernel)
+
+
 def _host(x):
     """a numpy operand as a contiguous array torch accepts (uint32 key data travels as int32 bits)"""
     a = np.asarray(x)
@@ -258,7 +270,7 @@ def replay_scratch_states(C, max_steps, pipelined=False):
 
 
 def _replay_plan(p, max_steps, rev_checkpoints, device):
-    kid, _ = _lib.kernel_id(p.kernel)
+    kid, _ = kernel_ref(p.kernel)
     info = _lib.kernel_info(kid)
     threads = info["sms"] * info["blocks_per_sm"] * info["block"]
     M = int(max_steps)
@@ -331,7 +343,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     kernel = p.kernel
     if p.vg_fallback is not None and known["rev_checkpoints"] < known["max_steps"]:
         kernel = p.vg_fallback          # (items may outgrow the head: the fused replay's checkpointed schedule)
-    kid, nbuf = _lib.kernel_id(kernel)
+    kid, nbuf = kernel_ref(kernel)
     ptrs = [0 if t is None else t.data_ptr() for t in args] + [t.data_ptr() for t in res]
     if len(ptrs) != nbuf:
         raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {kernel} takes {nbuf}")

@@ -7,6 +7,8 @@
 // the context-independent library API (cudaLibraryLoadData), so no per-context bookkeeping is needed.
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -237,6 +239,80 @@ int tm_register(int64_t id, const void* image, size_t n, const char* note, int32
   k.smem = smem_bytes;
   k.block = block;
   return TM_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ NVRTC
+// libnvrtc is opened on first use (the library itself does not link it, so it loads where NVRTC is absent)
+namespace {
+struct Nvrtc {
+  void* h = nullptr;
+  int (*create)(void**, const char*, const char*, int, const char* const*, const char* const*) = nullptr;
+  int (*compile)(void*, int, const char* const*) = nullptr;
+  int (*log_size)(void*, size_t*) = nullptr;
+  int (*log)(void*, char*) = nullptr;
+  int (*cubin_size)(void*, size_t*) = nullptr;
+  int (*cubin)(void*, char*) = nullptr;
+  int (*destroy)(void**) = nullptr;
+};
+Nvrtc g_nvrtc;
+
+int load_nvrtc() {
+  if (g_nvrtc.h) return TM_OK;
+  const char* names[] = {"libnvrtc.so.12", "libnvrtc.so", "/usr/local/cuda/lib64/libnvrtc.so.12"};
+  void* h = nullptr;
+  for (const char* n : names)
+    if ((h = dlopen(n, RTLD_NOW | RTLD_LOCAL))) break;
+  if (!h) return fail(TM_EINVAL, "tallymap_b200: NVRTC (libnvrtc.so.12) is not available: %s", dlerror());
+  Nvrtc f;
+  f.h = h;
+  f.create = reinterpret_cast<decltype(f.create)>(dlsym(h, "nvrtcCreateProgram"));
+  f.compile = reinterpret_cast<decltype(f.compile)>(dlsym(h, "nvrtcCompileProgram"));
+  f.log_size = reinterpret_cast<decltype(f.log_size)>(dlsym(h, "nvrtcGetProgramLogSize"));
+  f.log = reinterpret_cast<decltype(f.log)>(dlsym(h, "nvrtcGetProgramLog"));
+  f.cubin_size = reinterpret_cast<decltype(f.cubin_size)>(dlsym(h, "nvrtcGetCUBINSize"));
+  f.cubin = reinterpret_cast<decltype(f.cubin)>(dlsym(h, "nvrtcGetCUBIN"));
+  f.destroy = reinterpret_cast<decltype(f.destroy)>(dlsym(h, "nvrtcDestroyProgram"));
+  if (!f.create || !f.compile || !f.log_size || !f.log || !f.cubin_size || !f.cubin || !f.destroy)
+    return fail(TM_EINVAL, "tallymap_b200: libnvrtc lacks an entry point");
+  g_nvrtc = f;
+  return TM_OK;
+}
+}  // namespace
+
+int tm_compile_register(int64_t id, const char* source, const char* include_dir, const char* note,
+                        int32_t n_buffers, int32_t smem_bytes, int32_t block) {
+  if (!source || !include_dir) return fail(TM_EINVAL, "tallymap_b200: tm_compile_register: null argument");
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    init_registry();
+    if (find(id)) return TM_OK;       // already registered (first registration wins)
+    int rc = load_nvrtc();
+    if (rc) return rc;
+  }
+  void* prog = nullptr;
+  if (g_nvrtc.create(&prog, source, "tm_item.cu", 0, nullptr, nullptr) != 0 || !prog)
+    return fail(TM_EINVAL, "tallymap_b200: nvrtcCreateProgram failed");
+  const std::string inc = std::string("-I") + include_dir;
+  char blk[32];
+  std::snprintf(blk, sizeof(blk), "-DTM_BLOCK=%d", block);
+  const char* opts[] = {"-arch=sm_100a", "-std=c++17", "--fmad=false", "-lineinfo", inc.c_str(),
+                        "-I/usr/local/cuda/include", blk};
+  const int crc = g_nvrtc.compile(prog, 7, opts);
+  if (crc != 0) {
+    size_t n = 0;
+    g_nvrtc.log_size(prog, &n);
+    std::string log(n, '\0');
+    if (n) g_nvrtc.log(prog, &log[0]);
+    g_nvrtc.destroy(&prog);
+    return fail(TM_EINVAL, "tallymap_b200: NVRTC failed to compile '%s':\n%.3000s", note ? note : "", log.c_str());
+  }
+  size_t n = 0;
+  g_nvrtc.cubin_size(prog, &n);
+  std::vector<char> cubin(n);
+  if (n) g_nvrtc.cubin(prog, cubin.data());
+  g_nvrtc.destroy(&prog);
+  if (n == 0) return fail(TM_EINVAL, "tallymap_b200: NVRTC produced no cubin");
+  return tm_register(id, cubin.data(), n, note, n_buffers, smem_bytes, block);
 }
 
 int tm_kernel_info(int64_t id, long long* out) {

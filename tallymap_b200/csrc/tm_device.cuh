@@ -6,14 +6,25 @@
 // --fmad=false, so every f32 + - * below is one IEEE rounding, as the reference's NVRTC flags (-fmad=false,
 // backends/kernel/compile.py:27) and its host target (-ffp-contract=off) make it.
 #pragma once
+#ifdef __CUDACC_RTC__
+#include <cuda/std/cstdint>
+#else
 #include <cstdint>
+#endif
 
 namespace tmb {
 
+#ifdef __CUDACC_RTC__
+typedef cuda::std::int32_t i32;
+typedef cuda::std::uint32_t u32;
+typedef cuda::std::int64_t i64;
+typedef cuda::std::uint64_t u64;
+#else
 typedef int32_t i32;
 typedef uint32_t u32;
 typedef int64_t i64;
 typedef uint64_t u64;
+#endif
 
 // Kernel parameter block: every buffer pointer of a launch, args first then results (the layout of the reference's
 // SjParams, kernel.py:596 / shim.cc:36-40), passed by value.  TM_MAXP bounds the pointers a program may use.

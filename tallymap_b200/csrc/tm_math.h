@@ -15,8 +15,16 @@
 //         to r^19 / r^20, then the quadrant's sign and swap
 //   pow   x^y = exp(y log x) for x > 0 (the exponent's argument formed in double), IEEE special cases otherwise
 #pragma once
+#ifdef __CUDACC_RTC__
+#include <cuda/std/cstdint>
+typedef cuda::std::uint32_t uint32_t;
+typedef cuda::std::uint64_t uint64_t;
+typedef cuda::std::int32_t int32_t;
+typedef cuda::std::int64_t int64_t;
+#else
 #include <cstdint>
 #include <cstring>
+#endif
 
 #if defined(__CUDACC__)
 #define TM_HD __host__ __device__ __forceinline__

@@ -28,7 +28,13 @@
 //                                      emits, per-item results (the replay's truncation flag)
 //   void adj_flush(const Ctx&, unsigned char* smem, int tid, int nth)  (private accumulators -> shared -> global)
 #pragma once
+#ifdef __CUDACC_RTC__
+#include <cuda/std/type_traits>
+namespace tmstd = cuda::std;
+#else
 #include <type_traits>
+namespace tmstd = std;
+#endif
 
 #include "tm_device.cuh"
 
@@ -77,8 +83,10 @@ __device__ __forceinline__ void finish_block(const typename I::Ctx& cx, u32* ctl
 }
 
 // ------------------------------------------------------------------------------------------------ forward kernel
+// (each kernel is a __device__ body plus a __global__ wrapper, so that a program compiled at run time can wrap the
+// same body in an `extern "C"` entry point: see tallymap_b200/lower.py)
 template <class I>
-__global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const i64 n_items) {
+__device__ __forceinline__ void forward_body(const Params& P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
   I::setup(cx, P, smem);
@@ -120,13 +128,18 @@ __global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const
   finish_block<I>(cx, ctl);
 }
 
+template <class I>
+__global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const i64 n_items) {
+  forward_body<I>(P, n_items);
+}
+
 // An ITEM with `static constexpr bool kFused = true` is a value-and-gradient program (FusedVG below): its replay's
 // count pass is the forward pass itself, emitting the forward tallies (fwd_emit) and writing the forward's per-item
 // results (fwd_finish), so one launch yields the outputs and their gradient for cotangents given up front.
 template <class T, class = void>
-struct fused_trait : std::false_type {};
+struct fused_trait : tmstd::false_type {};
 template <class T>
-struct fused_trait<T, std::void_t<decltype(T::kFused)>> : std::integral_constant<bool, T::kFused> {};
+struct fused_trait<T, tmstd::void_t<decltype(T::kFused)>> : tmstd::integral_constant<bool, T::kFused> {};
 
 // ------------------------------------------------------------------------------------------------ replay kernel
 // The reverse-mode program of an item with one top-level loop: the checkpointed loop of tallymap/_reverse.py:324-444
@@ -151,7 +164,7 @@ struct fused_trait<T, std::void_t<decltype(T::kFused)>> : std::integral_constant
 // vjp(Ctx, const State& at, Adj&) (the step VJP at the state before the step); kReplay (the scratch buffer) and the
 // launch constants kConstM (max_steps), kConstC (C) and kConstThreads (threads the scratch holds).
 template <class I, int V>
-__global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const i64 n_items) {
+__device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
   I::setup(cx, P, smem);
@@ -293,6 +306,11 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
   finish_block<I>(cx, ctl);
 }
 
+template <class I, int V>
+__global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const i64 n_items) {
+  replay_body<I, V>(P, n_items);
+}
+
 // ------------------------------------------------------------------------------------------------ pipelined value and grad
 // vg_kernel<I, V>: a fused value-and-grad program (I::kFused) when every item fits the head (C >= max_steps).  In the
 // replay kernel a lane counts an item, then sweeps it, so at any iteration some lanes of a warp count and others
@@ -304,7 +322,7 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
 // Scratch: 2 (C + 1) states per thread.  ITEM additions: handoff(Ctx& sweep, const Ctx& count) gives the sweeping
 // context an item's per-item context while keeping its own per-thread accumulators.
 template <class I, int V>
-__global__ void __launch_bounds__(TM_BLOCK) vg_kernel(const Params P, const i64 n_items) {
+__device__ __forceinline__ void vg_body(const Params& P, const i64 n_items) {
   static_assert(fused_trait<I>::value, "vg_kernel runs fused value-and-grad programs");
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
@@ -388,6 +406,11 @@ __global__ void __launch_bounds__(TM_BLOCK) vg_kernel(const Params P, const i64 
   I::handoff(cs, cx);   // one context for the flush: the counting context's, with the sweeping one's accumulators
   I::adj_flush(cs, smem, threadIdx.x, blockDim.x);
   finish_block<I>(cs, ctl);
+}
+
+template <class I, int V>
+__global__ void __launch_bounds__(TM_BLOCK) vg_kernel(const Params P, const i64 n_items) {
+  vg_body<I, V>(P, n_items);
 }
 
 // ------------------------------------------------------------------------------------------------ value and grad

@@ -1,0 +1,154 @@
+"""The operations an item function may use, for tracing (tallymap_b200.trace): a scalar subset of jax.numpy,
+jax.random and lax.while_loop with jax's semantics, the ones the reference's op table lowers for these items
+(tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
+random_bits / fold_in / split, while).
+
+    from tallymap_b200 import lang as tl
+
+    def walk(t, x, key, drift):
+        def body(c):
+            k, x, t = c
+            u = tl.random.uniform(tl.random.fold_in(key, k))
+            t = t.add("hist", (x * 256).astype(tl.int32), drift * x)
+            return k + 1, x + 0.02 * (2 * u - 1), t
+        k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+        t = t.add("side", (x > 1).astype(tl.int32), 1.0)
+        return t, k
+
+Transcendentals are the backend's shared f32 math (identical on the host oracle and the device); f32 -> int32
+conversion truncates toward zero, saturating, NaN -> 0 (the reference's _rz conversions).
+"""
+from . import trace as T
+
+float32, int32, uint32, bool_ = "float32", "int32", "uint32", "bool"
+while_loop = T.while_loop
+
+
+def _un(prim, x, out=None):
+    x = T._lit(x)
+    if isinstance(x, T.Lit):
+        raise T.TraceError(f"tallymap_b200.lang.{prim} of a literal")
+    return T._cur().emit(prim, [x], [out or x.dtype])[0]
+
+
+def _f32(prim, x):
+    x = T._lit(x)
+    if x.dtype != T.F32:
+        raise T.TraceError(f"tallymap_b200.lang.{prim} takes float32")
+    return _un(prim, x)
+
+
+def log(x):
+    return _f32("log", x)
+
+
+def exp(x):
+    return _f32("exp", x)
+
+
+def sin(x):
+    return _f32("sin", x)
+
+
+def cos(x):
+    return _f32("cos", x)
+
+
+def sqrt(x):
+    return _f32("sqrt", x)
+
+
+def floor(x):
+    return _f32("floor", x)
+
+
+def abs(x):   # noqa: A001 (jnp.abs)
+    return _un("abs", x)
+
+
+def power(x, y):
+    x0 = x if isinstance(x, T.Var) else None
+    y0 = y if isinstance(y, T.Var) else None
+    x, y = T._lit(x, y0), T._lit(y, x0)
+    if x.dtype != T.F32 or y.dtype != T.F32:
+        raise T.TraceError("tallymap_b200.lang.power takes float32")
+    return T._cur().emit("pow", [x, y], [T.F32])[0]
+
+
+def maximum(a, b):
+    """jax.lax.max: NaN if either is NaN, max(-0, +0) = +0"""
+    return T._binary("max", a, b)
+
+
+def minimum(a, b):
+    return T._binary("min", a, b)
+
+
+def where(c, a, b):
+    c = T._lit(c)
+    if c.dtype != T.BOOL:
+        raise T.TraceError("tallymap_b200.lang.where: the condition must be bool")
+    a0 = a if isinstance(a, T.Var) else None
+    b0 = b if isinstance(b, T.Var) else None
+    a, b = T._lit(a, b0), T._lit(b, a0)
+    if a.dtype != b.dtype:
+        raise T.TraceError(f"tallymap_b200.lang.where of {a.dtype} and {b.dtype}")
+    return T._cur().emit("select", [c, a, b], [a.dtype])[0]
+
+
+class random:
+    """jax.random on raw uint32[2] key data, partitionable threefry (bitwise jax.random's)"""
+
+    @staticmethod
+    def _u32(x):
+        x = T._lit(x)
+        if x.dtype == T.I32:
+            x = x.astype(uint32) if isinstance(x, T.Var) else T.Lit(int(x.value) & 0xFFFFFFFF, T.U32)
+        if x.dtype != T.U32:
+            raise T.TraceError("tallymap_b200.lang.random: integer data expected")
+        return x
+
+    @staticmethod
+    def fold_in(key, data):
+        """jax.random.fold_in: threefry2x32(key, (0, data))"""
+        o = T._cur().emit("threefry", [key.a, key.b, T.Lit(0, T.U32), random._u32(data)], [T.U32, T.U32])
+        return T.Key(o[0], o[1])
+
+    @staticmethod
+    def split(key, num=2):
+        """jax.random.split(key, num): key i = threefry2x32(key, (0, i))"""
+        return tuple(random.fold_in(key, i) for i in range(int(num)))
+
+    @staticmethod
+    def bits(key, shape=()):
+        """jax.random.bits(key, shape, uint32): element i = o0 ^ o1 of threefry2x32(key, (0, i))"""
+        n = _count(shape)
+        out = tuple(T._cur().emit("bits", [key.a, key.b, T.Lit(i, T.U32)], [T.U32])[0] for i in range(n))
+        return out[0] if shape == () else out
+
+    @staticmethod
+    def uniform(key, shape=(), dtype=float32, minval=0.0, maxval=1.0):
+        """jax.random.uniform: the mantissa fill of random bits in [1, 2) minus 1, then max(lo, f * (hi - lo) + lo)"""
+        if dtype != float32:
+            raise T.TraceError("tallymap_b200.lang.random.uniform: float32 only")
+        n = _count(shape)
+        out = []
+        for i in range(n):
+            f = T._cur().emit("uniform01", [key.a, key.b, T.Lit(i, T.U32)], [T.F32])[0]
+            if not (isinstance(minval, float) and isinstance(maxval, float) and minval == 0.0 and maxval == 1.0):
+                # jax computes max(lo, f * (hi - lo) + lo); for lo = 0, hi = 1 that is f itself, bitwise
+                lo, hi = minval, maxval
+                f = maximum(lo, f * (hi - lo) + lo) if isinstance(hi, T.Var) or isinstance(lo, T.Var) \
+                    else maximum(float(lo), f * float(hi - lo) + float(lo))
+            out.append(f)
+        return out[0] if shape == () else tuple(out)
+
+
+def _count(shape):
+    if shape == ():
+        return 1
+    if isinstance(shape, int):
+        shape = (shape,)
+    if len(shape) != 1:
+        raise T.TraceError("tallymap_b200.lang.random: shape () or (n,)")
+    return int(shape[0])

@@ -1,0 +1,825 @@
+"""Lowering of a traced item (tallymap_b200.trace.Traced) to CUDA C for the persistent-thread runtime, and its
+compilation at run time (NVRTC, sm_100a) into a registered kernel.
+
+The reference lowers an item jaxpr to straight-line C inside its generated kernel (backends/kernel/kernel.py:428-451,
+codegen.py:494-980) and compiles with NVRTC (backends/kernel/compile.py:160-173).  Here the item becomes an ITEM
+struct of the hand-written runtime (csrc/tm_runtime.cuh): the pre-loop code is `start`, the loop predicate `cond`, the
+loop body `step`, the post-loop code `finish` -- the step schedule of kernel.py:225-295, which needs exactly one
+top-level loop.  Its reverse mode is the replay adjoint of _reverse.py:1079-1180 (vjp_prog): the same runtime's
+replay_kernel with a generated step VJP (reverse mode over the body's equations, only for float values that depend on
+a differentiated operand: _reverse.py:208 `_active`), the broadcast cotangents summed per item in f32 and emitted once
+into an exact tally.
+
+Launch layouts are the backend's (backend.ItemProgram): forward = [per-item][broadcast][consts i32[1]][order] |
+[tallies][ctl][stats] | [per-item results][truncated]; reverse = [per-item][broadcast][output cotangents][consts
+i32[3]][order] | [g f32[W]][exact words][ctl][stats] | [truncated][replay scratch].
+"""
+import ctypes
+import hashlib
+import os
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import trace as T
+
+CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
+PRIV_BYTES = 4096        # outputs up to this size are privatised per block in shared memory (kernel.py:300)
+CTYPE = {T.F32: "float", T.I32: "i32", T.U32: "u32", T.BOOL: "bool"}
+TDTYPE = {T.F32: torch.float32, T.I32: torch.int32, T.U32: torch.int32, T.BOOL: torch.uint8}
+
+
+class LowerError(TypeError):
+    pass
+
+
+# ------------------------------------------------------------------------------------------------ C expressions
+def c_lit(lit):
+    if lit.dtype == T.F32:
+        v = float(np.float32(lit.value))
+        if np.isnan(v):
+            return "__int_as_float(0x7fc00000)"
+        if np.isinf(v):
+            return "__int_as_float(0x7f800000)" if v > 0 else "__int_as_float((int)0xff800000u)"
+        return float(v).hex() + "f"
+    if lit.dtype == T.I32:
+        v = int(lit.value)
+        return "(i32)(-2147483647 - 1)" if v == -2 ** 31 else f"(i32){v}"
+    if lit.dtype == T.U32:
+        return f"{int(lit.value) & 0xFFFFFFFF}u"
+    return "true" if lit.value else "false"
+
+
+_BIN = {"add": "+", "sub": "-", "mul": "*", "div": "/", "lt": "<", "le": "<=", "gt": ">", "ge": ">=", "eq": "==",
+        "ne": "!="}
+_MATH = {"log": "tmm::logf", "exp": "tmm::expf", "sin": "tmm::sinf", "cos": "tmm::cosf"}
+
+
+def c_expr(e, a):
+    """the C expression of equation e's single output; a: its inputs' C expressions"""
+    p, d = e.prim, e.ins[0].dtype if e.ins else None
+    if p in ("add", "sub", "mul") and d in (T.I32,):
+        return f"(i32)((u32)({a[0]}) {_BIN[p]} (u32)({a[1]}))"         # wrapping int32 arithmetic
+    if p in _BIN:
+        return f"({a[0]} {_BIN[p]} {a[1]})"
+    if p == "idiv":
+        return f"tm_floordiv({a[0]}, {a[1]})"
+    if p == "irem":
+        return f"tm_floormod({a[0]}, {a[1]})"
+    if p == "neg":
+        return f"(-{a[0]})" if d == T.F32 else f"(i32)(0u - (u32)({a[0]}))"
+    if p in ("and", "or", "xor"):
+        op = {"and": "&", "or": "|", "xor": "^"}[p]
+        return f"({a[0]} {op} {a[1]})" if d != T.BOOL else f"({a[0]} {op} {a[1]})"
+    if p == "not":
+        return f"(!{a[0]})" if d == T.BOOL else f"(~{a[0]})"
+    if p in _MATH:
+        return f"{_MATH[p]}({a[0]})"
+    if p == "sqrt":
+        return f"__fsqrt_rn({a[0]})"
+    if p == "floor":
+        return f"floorf({a[0]})"
+    if p == "abs":
+        return f"fabsf({a[0]})" if d == T.F32 else f"tm_iabs({a[0]})"
+    if p == "pow":
+        return f"tmm::powf({a[0]}, {a[1]})"
+    if p == "max":
+        return f"tm_max({a[0]}, {a[1]})"
+    if p == "min":
+        return f"tm_min({a[0]}, {a[1]})"
+    if p == "select":
+        return f"({a[0]} ? {a[1]} : {a[2]})"
+    if p == "inrange":
+        return f"((u32)({a[0]}) < {int(e.params['n'])}u)"
+    if p == "convert":
+        return _convert(d, e.outs[0].dtype, a[0])
+    if p == "bits":
+        return f"random_bits32(Key{{{a[0]}, {a[1]}}}, {a[2]})"
+    if p == "uniform01":
+        return f"uniform01(Key{{{a[0]}, {a[1]}}}, {a[2]})"
+    raise LowerError(f"tallymap_b200.lower: no lowering for {p}")
+
+
+def _convert(src, dst, x):
+    if src == T.F32:
+        return {T.I32: f"f2i({x})", T.U32: f"__float2uint_rz({x})", T.BOOL: f"({x} != 0.0f)"}[dst]
+    if src == T.I32:
+        return {T.F32: f"__int2float_rn({x})", T.U32: f"(u32)({x})", T.BOOL: f"({x} != 0)"}[dst]
+    if src == T.U32:
+        return {T.F32: f"__uint2float_rn({x})", T.I32: f"(i32)({x})", T.BOOL: f"({x} != 0u)"}[dst]
+    return {T.F32: f"({x} ? 1.0f : 0.0f)", T.I32: f"(i32)({x})", T.U32: f"(u32)({x})"}[dst]
+
+
+PRELUDE = r"""
+#include "tm_tally.cuh"
+#include "tm_math.h"
+namespace tmb {
+__device__ __forceinline__ float tm_max(float a, float b) {   // lax.max: NaN wins, max(-0, +0) = +0
+  return (a > b || a != a) ? a : ((b > a || b != b) ? b : (a == 0.0f ? a + b : a));
+}
+__device__ __forceinline__ float tm_min(float a, float b) {   // lax.min: NaN wins, min(-0, +0) = -0
+  return (a < b || a != a) ? a : ((b < a || b != b) ? b : (a == 0.0f ? -((-a) + (-b)) : a));
+}
+__device__ __forceinline__ i32 tm_max(i32 a, i32 b) { return a > b ? a : b; }
+__device__ __forceinline__ i32 tm_min(i32 a, i32 b) { return a < b ? a : b; }
+__device__ __forceinline__ i32 tm_iabs(i32 a) { return a < 0 ? (i32)(0u - (u32)a) : a; }
+__device__ __forceinline__ i32 tm_floordiv(i32 a, i32 b) {   // jnp.floor_divide; x // 0 = 0 here
+  if (b == 0) return 0;
+  if (b == -1) return (i32)(0u - (u32)a);
+  const i32 q = a / b;
+  return (q * b != a && ((a < 0) != (b < 0))) ? q - 1 : q;
+}
+__device__ __forceinline__ i32 tm_floormod(i32 a, i32 b) {
+  if (b == 0 || b == -1) return 0;
+  const i32 r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
+}
+__device__ __forceinline__ u32 tm_floordiv(u32 a, u32 b) { return b ? a / b : 0u; }
+__device__ __forceinline__ u32 tm_floormod(u32 a, u32 b) { return b ? a % b : 0u; }
+}  // namespace tmb
+"""
+
+
+# ------------------------------------------------------------------------------------------------ program analysis
+def _ids(xs):
+    return {x.id for x in xs if isinstance(x, T.Var)}
+
+
+def _uses(eqns):
+    u = set()
+    for e in eqns:
+        u |= _ids(e.ins)
+    return u
+
+
+def _defs(eqns):
+    d = set()
+    for e in eqns:
+        d |= _ids(e.outs)
+    return d
+
+
+class Item:
+    """the layout facts of a traced item shared by its forward and reverse lowering"""
+
+    def __init__(self, tr, in_specs, name):
+        self.tr, self.name = tr, name
+        self.in_specs = list(in_specs)
+        npi = tr.n_per_item
+        self.pi, self.bc = tr.inputs[:npi], tr.inputs[npi:]
+        for b in self.bc:
+            if not isinstance(b, T.Var):
+                raise LowerError("tallymap_b200.lower: broadcast operands are scalars")
+        if any(e.prim == "emit" for e in tr.cond):
+            raise LowerError("tallymap_b200.lower: the loop condition may not emit")
+        self.specs = list(tr.specs.items())     # [(name, (shape, dtype))]
+        # the per-item input variables, each with its loader
+        self.loads = []                         # (var, C expression with `item`)
+        for j, (x, s) in enumerate(zip(self.pi, self.in_specs[:npi])):
+            if isinstance(x, T.Key):
+                self.loads += [(x.a, f"__ldg(&c.in{j}[item]).x"), (x.b, f"__ldg(&c.in{j}[item]).y")]
+            elif isinstance(x, tuple):
+                self.loads += [(v, f"__ldg(&c.in{j}[item * {len(x)} + {i}])") for i, v in enumerate(x)]
+            else:
+                self.loads.append((x, f"__ldg(&c.in{j}[item])"))
+        self.bc_ids = {b.id: k for k, b in enumerate(self.bc)}
+        # step counters: carries that start at 0 and gain 1 per step equal the step index (not stored by the replay)
+        self.counter = set()
+        by_id = {o.id: e for e in tr.body for o in e.outs}
+        for j, (ci, co) in enumerate(zip(tr.carry_in, tr.body_out)):
+            if isinstance(ci, T.Lit) and ci.dtype == T.I32 and ci.value == 0 and isinstance(co, T.Var):
+                e = by_id.get(co.id)
+                if e is not None and e.prim == "add" and len(e.ins) == 2 and isinstance(e.ins[0], T.Var) and \
+                        e.ins[0].id == tr.carry[j].id and isinstance(e.ins[1], T.Lit) and e.ins[1].value == 1:
+                    self.counter.add(j)
+        # pre-loop values (inputs included) that later code reads: kept in the per-thread context
+        later = _uses(tr.cond) | _uses(tr.body) | _uses(tr.post) | _ids(tr.body_out) | _ids(tr.results) | \
+            _ids([tr.cond_out])
+        pre_defined = _defs(tr.pre) | {v.id for v, _ in self.loads}
+        self.saved = sorted(later & pre_defined)
+        self.vars = {}
+        for v, _ in self.loads:
+            self.vars[v.id] = v
+        for e in tr.pre + tr.cond + tr.body + tr.post:
+            for o in e.outs:
+                self.vars[o.id] = o
+        for b in self.bc:
+            self.vars[b.id] = b
+        for v in tr.carry + tr.post_carry:
+            self.vars[v.id] = v
+
+
+def _names_pre(it):
+    """C names in start(): locals for everything"""
+    return {i: f"v{i}" for i in it.vars} | {i: f"c.b{k}" for i, k in it.bc_ids.items()}
+
+
+def _names_loop(it, carry, state="s"):
+    n = {i: f"c.p{i}" for i in it.saved} | {i: f"c.b{k}" for i, k in it.bc_ids.items()}
+    for j, v in enumerate(carry):
+        n[v.id] = f"{state}.c{j}"
+    return n
+
+
+def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False):
+    """straight-line C for eqns; names: id -> C expression (updated with the locals defined here)"""
+    out = []
+    for e in eqns:
+        a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        if e.prim == "emit":
+            if not skip_emits:
+                out.append(indent + emitter(e.params["tally"], a[0], a[1]))
+            continue
+        if e.prim == "threefry":
+            o0, o1 = e.outs
+            out.append(f"{indent}u32 v{o0.id}, v{o1.id};")
+            out.append(f"{indent}threefry2x32({a[0]}, {a[1]}, {a[2]}, {a[3]}, v{o0.id}, v{o1.id});")
+            names[o0.id], names[o1.id] = f"v{o0.id}", f"v{o1.id}"
+            continue
+        o = e.outs[0]
+        out.append(f"{indent}const {CTYPE[o.dtype]} v{o.id} = {c_expr(e, a)};")
+        names[o.id] = f"v{o.id}"
+    return out
+
+
+def _ref(x, names):
+    return names[x.id] if isinstance(x, T.Var) else c_lit(x)
+
+
+# ------------------------------------------------------------------------------------------------ forward program
+def forward_source(it):
+    """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes, tally layout)"""
+    tr = it.tr
+    npi, nbc = len(it.pi), len(it.bc)
+    lines = [PRELUDE, "namespace tmb {", "struct GenFwd {"]
+    # buffer indices: per-item, broadcast, consts, order | tallies, ctl, stats | ys, trunc
+    idx = 0
+    enum = []
+    for j in range(npi):
+        enum.append(f"kIn{j} = {idx}"); idx += 1
+    for k in range(nbc):
+        enum.append(f"kBc{k} = {idx}"); idx += 1
+    enum.append(f"kConsts = {idx}"); idx += 1
+    enum.append(f"kOrder = {idx}"); idx += 1
+    for t, _ in enumerate(it.specs):
+        enum.append(f"kT{t} = {idx}"); idx += 1
+    enum.append(f"kCtl = {idx}"); idx += 1
+    enum.append(f"kStats = {idx}"); idx += 1
+    for r in range(len(tr.results)):
+        enum.append(f"kY{r} = {idx}"); idx += 1
+    enum.append(f"kTrunc = {idx}"); idx += 1
+    enum.append(f"kNBuf = {idx}")
+    lines.append("  enum { " + ", ".join(enum) + " };")
+    # privatised tallies
+    smem, priv = 0, {}
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        if S * 4 <= PRIV_BYTES:
+            priv[name] = (t, smem, S, dt)
+            smem += S * 4
+    lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
+    # context
+    ctx = ["  struct Ctx {"]
+    for j, s in enumerate(it.in_specs[:npi]):
+        ctx.append(f"    const {_in_ctype(s)}* in{j};")
+    for k, b in enumerate(it.bc):
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+    ctx.append("    i32 M;")
+    ctx.append("    i32* stats;")
+    tinfo = {}
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        ct = "float" if dt == T.F32 else "i32"
+        ctx.append(f"    {ct}* g{t};")
+        if name in priv:
+            ctx.append(f"    {ct}* s{t};")
+        tinfo[name] = (t, S, dt, name in priv)
+    for r, y in enumerate(tr.results):
+        ctx.append(f"    {CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}* y{r};")
+    ctx.append("    uint8_t* trunc;")
+    for i in it.saved:
+        ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
+    ctx.append("  };")
+    lines += ctx
+    lines.append("  struct State {")
+    lines.append("    i32 kc;")
+    for j, v in enumerate(tr.carry):
+        lines.append(f"    {CTYPE[v.dtype]} c{j};")
+    lines.append("  };")
+    # setup
+    lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
+    for j, s in enumerate(it.in_specs[:npi]):
+        lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
+    for k, b in enumerate(it.bc):
+        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+    lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
+    lines.append("    c.stats = static_cast<i32*>(P.p[kStats]);")
+    for name, (t, S, dt, pv) in tinfo.items():
+        ct = "float" if dt == T.F32 else "i32"
+        lines.append(f"    c.g{t} = static_cast<{ct}*>(P.p[kT{t}]);")
+        if pv:
+            lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[name][1]});")
+    for r, y in enumerate(tr.results):
+        lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
+    lines.append("    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);")
+    lines.append("  }")
+    lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
+
+    def emitter(name, idx_c, v_c):
+        t, S, dt, pv = tinfo[name]
+        if dt == T.F32:
+            if pv:
+                return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
+            return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
+                    f"else fatom(&c.g{t}[b_], {v_c}); }}")
+        tgt = f"c.s{t}" if pv else f"c.g{t}"
+        return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
+                f"else if ({v_c}) atomicAdd(&{tgt}[b_], {v_c}); }}")
+
+    # start: inputs, pre-loop code, the saved values, the initial carry
+    lines.append("  __device__ static State start(Ctx& c, i64 item) {")
+    names = _names_pre(it)
+    for v, ld in it.loads:
+        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    lines += _emit_code(tr.pre, names, emitter)
+    for i in it.saved:
+        lines.append(f"    c.p{i} = {names[i]};")
+    lines.append("    State s;")
+    lines.append("    s.kc = 0;")
+    for j, x in enumerate(tr.carry_in):
+        lines.append(f"    s.c{j} = {_ref(x, names)};")
+    lines.append("    return s;")
+    lines.append("  }")
+    lines += _pred_fn(it)
+    lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
+    lines.append("    return s.kc < c.M && pred(c, s);")
+    lines.append("  }")
+    lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
+    names = _names_loop(it, tr.carry)
+    lines += _emit_code(tr.body, names, emitter)
+    lines += _assign_carry(it, names)
+    lines.append("  }")
+    lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    names = _names_loop(it, tr.post_carry)
+    lines += _emit_code(tr.post, names, emitter)
+    for r, y in enumerate(tr.results):
+        lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
+    lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
+    lines.append("  }")
+    lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
+    for name, (t, S, dt, pv) in tinfo.items():
+        if not pv:
+            continue
+        if dt == T.F32:
+            lines.append(f"    SumPriv<{S}>::flush(c.s{t}, c.g{t}, tid, nth);")
+        else:
+            lines.append(f"    for (int b = tid; b < {S}; b += nth) if (c.s{t}[b]) atomicAdd(&c.g{t}[b], c.s{t}[b]);")
+    lines.append("  }")
+    lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
+    lines.append("};")
+    lines.append("}  // namespace tmb")
+    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append("  tmb::forward_body<tmb::GenFwd>(P, n);")
+    lines.append("}")
+    return "\n".join(lines), max(smem, 16)
+
+
+def _in_ctype(s):
+    if s == "key":
+        return "uint2"
+    if isinstance(s, tuple):
+        return CTYPE[s[0]]
+    return CTYPE[s]
+
+
+def _pred_fn(it):
+    tr = it.tr
+    out = ["  __device__ __forceinline__ static bool pred(const Ctx& c, const State& s) {"]
+    names = _names_loop(it, tr.carry)
+    out += _emit_code(tr.cond, names, None)
+    out.append(f"    return {_ref(tr.cond_out, names)};")
+    out.append("  }")
+    return out
+
+
+def _assign_carry(it, names, state="s"):
+    tr = it.tr
+    out = []
+    for j, x in enumerate(tr.body_out):
+        out.append(f"    const {CTYPE[tr.carry[j].dtype]} n{j} = {_ref(x, names)};")
+    for j in range(len(tr.body_out)):
+        out.append(f"    {state}.c{j} = n{j};")
+    out.append(f"    {state}.kc += 1;")
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ compilation
+_COMPILED = {}
+
+
+def compile_kernel(source, note, n_buffers, smem_bytes):
+    """compile `source` (its entry point `tm_main`) for sm_100a with NVRTC and register it -> kernel id.  Cached per
+    process by the source's digest (the reference's structural kernel cache, backends/kernel/__init__.py:71-128)."""
+    digest = hashlib.sha256(source.encode()).hexdigest()
+    kid = int(digest[:15], 16)          # a positive int64 id
+    if kid in _COMPILED:
+        return kid
+    L = _lib.lib()
+    _lib.check(L.tm_compile_register(ctypes.c_int64(kid), source.encode(), CSRC.encode(), note.encode(),
+                                     n_buffers, smem_bytes, 128))
+    _COMPILED[kid] = note
+    from . import backend
+    backend.COMPILED[kid] = n_buffers
+    return kid
+
+
+# ------------------------------------------------------------------------------------------------ reverse program
+def _active(it, wrt):
+    """float variables that depend on the differentiated broadcast operands (tallymap/_reverse.py:208 `_active`)"""
+    tr = it.tr
+    act = {it.bc[k].id for k in wrt if it.bc[k].dtype == T.F32}
+
+    def prop(eqns):
+        for e in eqns:
+            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor") or not e.outs:
+                continue
+            if any(isinstance(x, T.Var) and x.id in act for x in e.ins):
+                for o in e.outs:
+                    if o.dtype == T.F32:
+                        act.add(o.id)
+    prop(tr.pre)
+    carry_act = [isinstance(x, T.Var) and x.id in act for x in tr.carry_in]
+    while True:
+        for j, v in enumerate(tr.carry):
+            if carry_act[j] and v.dtype == T.F32:
+                act.add(v.id)
+        prop(tr.body)
+        new = [carry_act[j] or (isinstance(x, T.Var) and x.id in act) for j, x in enumerate(tr.body_out)]
+        if new == carry_act:
+            break
+        carry_act = new
+    for j, v in enumerate(tr.post_carry):
+        if carry_act[j] and v.dtype == T.F32:
+            act.add(v.id)
+    prop(tr.post)
+    return act, [carry_act[j] and tr.carry[j].dtype == T.F32 for j in range(len(tr.carry))]
+
+
+class _Rev:
+    """reverse-mode code for a straight-line equation list: cotangent locals, first contribution assigned, later ones
+    added (jax's add_jaxvals order)"""
+
+    def __init__(self, active, indent="    ", tag="g"):
+        self.active, self.ct, self.lines, self.indent, self.tag = active, {}, [], indent, tag
+        self.n = 0
+
+    def add(self, x, expr):
+        if not isinstance(x, T.Var) or x.id not in self.active:
+            return
+        if x.id in self.ct:
+            nm = self.ct[x.id]
+            self.lines.append(f"{self.indent}{nm} = {nm} + {expr};")
+        else:
+            self.n += 1
+            nm = f"{self.tag}{x.id}_{self.n}"
+            self.lines.append(f"{self.indent}float {nm} = {expr};")
+            self.ct[x.id] = nm
+
+    def run(self, eqns, names, ct_tally):
+        for e in reversed(eqns):
+            if e.prim == "emit":
+                idx, v = e.ins
+                if isinstance(v, T.Var) and v.id in self.active and e.params["tally"] in ct_tally:
+                    ptr, S = ct_tally[e.params["tally"]][:2]
+                    i = _ref(idx, names)
+                    self.add(v, f"(((u32)({i}) < {S}u) ? {ptr}[{i}] : 0.0f)")
+                continue
+            if not e.outs or e.outs[0].id not in self.ct:
+                continue
+            self.rule(e, self.ct[e.outs[0].id], [_ref(x, names) for x in e.ins], names)
+
+    def rule(self, e, g, a, names):
+        p, x = e.prim, e.ins
+        out = names.get(e.outs[0].id, f"v{e.outs[0].id}")
+        if p == "add":
+            self.add(x[0], g)
+            self.add(x[1], g)
+        elif p == "sub":
+            self.add(x[0], g)
+            self.add(x[1], f"(-{g})")
+        elif p == "mul":
+            self.add(x[0], f"({g} * {a[1]})")
+            self.add(x[1], f"({a[0]} * {g})")
+        elif p == "div":
+            self.add(x[0], f"({g} / {a[1]})")
+            self.add(x[1], f"(((-{g}) * {a[0]}) * (1.0f / ({a[1]} * {a[1]})))")
+        elif p == "neg":
+            self.add(x[0], f"(-{g})")
+        elif p == "log":
+            self.add(x[0], f"({g} / {a[0]})")
+        elif p == "exp":
+            self.add(x[0], f"({g} * {out})")
+        elif p == "sin":
+            self.add(x[0], f"({g} * tmm::cosf({a[0]}))")
+        elif p == "cos":
+            self.add(x[0], f"((-{g}) * tmm::sinf({a[0]}))")
+        elif p == "sqrt":
+            self.add(x[0], f"({g} * (0.5f / {out}))")
+        elif p == "pow":
+            self.add(x[0], f"({g} * ({a[1]} * tmm::powf({a[0]}, {a[1]} - 1.0f)))")
+            self.add(x[1], f"({g} * (tmm::logf({a[0]}) * {out}))")
+        elif p == "abs":
+            self.add(x[0], f"({g} * ({a[0]} > 0.0f ? 1.0f : ({a[0]} < 0.0f ? -1.0f : 0.0f)))")
+        elif p in ("max", "min"):
+            # lax.max / min: the cotangent goes to the selected operand, half each on a tie (_balanced_eq)
+            self.add(x[0], f"({g} * ({a[0]} == {out} ? ({a[1]} == {out} ? 0.5f : 1.0f) : 0.0f))")
+            self.add(x[1], f"({g} * ({a[1]} == {out} ? ({a[0]} == {out} ? 0.5f : 1.0f) : 0.0f))")
+        elif p == "select":
+            self.add(x[1], f"({a[0]} ? {g} : 0.0f)")
+            self.add(x[2], f"({a[0]} ? 0.0f : {g})")
+        elif p == "convert":
+            if x[0].dtype == T.F32 and e.outs[0].dtype == T.F32:
+                self.add(x[0], g)
+        elif p == "floor":
+            pass
+        else:
+            raise LowerError(f"tallymap_b200.lower: no reverse rule for {p}")
+
+
+def grad_source(it, wrt):
+    """-> (C source of the replay ITEM for d <ct, outputs> / d bc[wrt], shared-memory bytes, stored-state bytes)"""
+    tr = it.tr
+    npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
+    act, carry_act = _active(it, wrt)
+    ftal = [(t, name, shape) for t, (name, (shape, dt)) in enumerate(it.specs) if dt == T.F32]
+    lines = [PRELUDE, "namespace tmb {", "struct GenGrad {"]
+    idx = 0
+    enum = []
+    for j in range(npi):
+        enum.append(f"kIn{j} = {idx}"); idx += 1
+    for k in range(nbc):
+        enum.append(f"kBc{k} = {idx}"); idx += 1
+    for q, (t, name, shape) in enumerate(ftal):
+        enum.append(f"kCt{q} = {idx}"); idx += 1
+    for nm in ("kConsts", "kOrder", "kG", "kExact", "kCtl", "kStats", "kTrunc", "kReplay"):
+        enum.append(f"{nm} = {idx}"); idx += 1
+    enum.append(f"kNBuf = {idx}")
+    lines.append("  enum { " + ", ".join(enum) + " };")
+    lines.append("  enum { kConstM = 0, kConstC = 1, kConstThreads = 2 };")
+    # output cotangents: staged in shared memory when small
+    smem = f"ExactBins<{W}>::kSmemBytes"
+    off = 0
+    ct_tally = {}
+    stage_lines = []
+    ctx_ct = []
+    for q, (t, name, shape) in enumerate(ftal):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        if S * 4 <= PRIV_BYTES:
+            ctx_ct.append(f"    const float* ct{q};")
+            stage_lines.append(f"    {{ const float* src = static_cast<const float*>(P.p[kCt{q}]); "
+                               f"float* d = reinterpret_cast<float*>(smem + ExactBins<{W}>::kSmemBytes + {off}); "
+                               f"for (int b = threadIdx.x; b < {S}; b += blockDim.x) d[b] = __ldg(&src[b]); }}")
+            ct_tally[name] = (f"c.ct{q}", S, off)
+            off += S * 4
+        else:
+            ctx_ct.append(f"    const float* ct{q};")
+            ct_tally[name] = (f"c.ct{q}", S, None)
+    lines.append(f"  static constexpr int kSmemBytes = {smem} + {off};")
+    smem_bytes = W * 5 * 8 + ((W * 4 + 7) // 8) * 8 + off       # (ExactBins<W>::kSmemBytes + the staged cotangents)
+    ctx = ["  struct Ctx {"]
+    for j, s in enumerate(it.in_specs[:npi]):
+        ctx.append(f"    const {_in_ctype(s)}* in{j};")
+    for k, b in enumerate(it.bc):
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+    ctx += ["    i32 M;", "    i32* stats;", "    u64* gw;", "    float* g;", "    uint8_t* trunc;"]
+    ctx += ctx_ct
+    for i in it.saved:
+        ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
+    ctx.append(f"    mutable ExactPriv<{W}> pv;")
+    ctx.append("  };")
+    lines += ctx
+    lines.append("  struct State {")
+    lines.append("    i32 kc;")
+    for j, v in enumerate(tr.carry):
+        lines.append(f"    {CTYPE[v.dtype]} c{j};")
+    lines.append("  };")
+    stored = [j for j in range(len(tr.carry)) if j not in it.counter]
+    lines.append("  struct Stored {")
+    for j in stored:
+        lines.append(f"    {CTYPE[tr.carry[j].dtype]} c{j};")
+    if not stored:
+        lines.append("    u32 unused;")
+    lines.append("  };")
+    stored_bytes = max(4, sum(4 for _ in stored))
+    act_saved = [i for i in it.saved if i in act]
+    lines.append("  struct Adj {")
+    for j, a in enumerate(carry_act):
+        if a:
+            lines.append(f"    float cc{j};")
+    for q in range(W):
+        lines.append(f"    float cb{q};   // loop's cotangent of bc[{wrt[q]}], summed newest step first")
+        lines.append(f"    float pb{q};   // the post-loop code's")
+    for i in act_saved:
+        lines.append(f"    float cp{i};")
+    lines.append("    bool has_post;")
+    lines.append("  };")
+    # setup / stage
+    lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
+    for j, s in enumerate(it.in_specs[:npi]):
+        lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
+    for k, b in enumerate(it.bc):
+        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+    lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
+    lines += ["    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.gw = static_cast<u64*>(P.p[kExact]);",
+              "    c.g = static_cast<float*>(P.p[kG]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
+    for q, (t, name, shape) in enumerate(ftal):
+        ptr, S, o = ct_tally[name]
+        if o is not None:
+            lines.append(f"    c.ct{q} = reinterpret_cast<const float*>(smem + ExactBins<{W}>::kSmemBytes + {o});")
+        else:
+            lines.append(f"    c.ct{q} = static_cast<const float*>(P.p[kCt{q}]);")
+    lines.append("    c.pv.zero();")
+    lines.append("  }")
+    lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
+    lines += stage_lines
+    lines.append("  }")
+    # start: pre-loop code without emits
+    lines.append("  __device__ static State start(Ctx& c, i64 item) {")
+    names = _names_pre(it)
+    for v, ld in it.loads:
+        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    lines += _emit_code(tr.pre, names, None, skip_emits=True)
+    for i in it.saved:
+        lines.append(f"    c.p{i} = {names[i]};")
+    lines += ["    State s;", "    s.kc = 0;"]
+    for j, x in enumerate(tr.carry_in):
+        lines.append(f"    s.c{j} = {_ref(x, names)};")
+    lines += ["    return s;", "  }"]
+    lines += _pred_fn(it)
+    lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
+    lines.append("    return s.kc < c.M && pred(c, s);")
+    lines.append("  }")
+    lines.append("  __device__ static void adj_start(const Ctx&, Adj& a) {")
+    for j, a_ in enumerate(carry_act):
+        if a_:
+            lines.append(f"    a.cc{j} = 0.0f;")
+    for q in range(W):
+        lines.append(f"    a.cb{q} = 0.0f;")
+        lines.append(f"    a.pb{q} = 0.0f;")
+    for i in act_saved:
+        lines.append(f"    a.cp{i} = 0.0f;")
+    lines.append("    a.has_post = false;")
+    lines.append("  }")
+    lines.append("  __device__ __forceinline__ static Stored store(const State& s) {")
+    lines.append("    Stored o;")
+    for j in stored:
+        lines.append(f"    o.c{j} = s.c{j};")
+    if not stored:
+        lines.append("    o.unused = 0u;")
+    lines += ["    return o;", "  }"]
+    lines.append("  __device__ __forceinline__ static State restore(const Ctx&, const Stored& o, i64 step) {")
+    lines += ["    State s;", "    s.kc = (i32)step;"]
+    for j in range(len(tr.carry)):
+        lines.append(f"    s.c{j} = {'(i32)step' if j in it.counter else f'o.c{j}'};")
+    lines += ["    return s;", "  }"]
+    lines.append("  __device__ __forceinline__ static void fwd(const Ctx& c, State& s) {")
+    names = _names_loop(it, tr.carry)
+    lines += _emit_code(tr.body, names, None, skip_emits=True)
+    lines += _assign_carry(it, names)
+    lines.append("  }")
+    bc_pos = {it.bc[k].id: q for q, k in enumerate(wrt)}
+
+    def finish_rev(rev, state_carry, into_carry, bc_field, extra=""):
+        """after a reverse run: carry cotangents (into_carry: assign a.cc from the carry variables' cotangents),
+        broadcast and saved-pre cotangents"""
+        out = []
+        if into_carry:
+            for j, a_ in enumerate(carry_act):
+                if a_:
+                    v = state_carry[j]
+                    out.append(f"    a.cc{j} = {rev.ct.get(v.id, '0.0f')};")
+        for bid, q in bc_pos.items():
+            if bid in rev.ct:
+                out.append(f"    a.{bc_field}{q} = a.{bc_field}{q} + {rev.ct[bid]};")
+        for i in act_saved:
+            if i in rev.ct:
+                out.append(f"    a.cp{i} = a.cp{i} + {rev.ct[i]};")
+        return out
+
+    # the step VJP at the state before the step
+    lines.append("  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {")
+    names = _names_loop(it, tr.carry, "at")
+    lines += _emit_code(tr.body, names, None, skip_emits=True)
+    rev = _Rev(act)
+    for j, x in enumerate(tr.body_out):
+        if carry_act[j]:
+            rev.add(x, f"a.cc{j}")
+    rev.run(tr.body, names, ct_tally)
+    lines += rev.lines
+    lines += finish_rev(rev, tr.carry, True, "cb")
+    lines.append("  }")
+    # the post-loop code's VJP: the loop outputs' cotangents
+    lines.append("  __device__ static void post_vjp(const Ctx& c, const State& fin, Adj& a) {")
+    names = _names_loop(it, tr.post_carry, "fin")
+    lines += _emit_code(tr.post, names, None, skip_emits=True)
+    rev = _Rev(act)
+    rev.run(tr.post, names, ct_tally)
+    lines += rev.lines
+    lines += finish_rev(rev, tr.post_carry, True, "pb")
+    if any(bid in rev.ct for bid in bc_pos):
+        lines.append("    a.has_post = true;")
+    lines.append("  }")
+    # the pre-loop code's VJP, then the item's emits
+    lines.append("  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {")
+    names = _names_pre(it)
+    for v, ld in it.loads:
+        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    lines += _emit_code(tr.pre, names, None, skip_emits=True)
+    rev = _Rev(act, tag="h")
+    for j, x in enumerate(tr.carry_in):
+        if carry_act[j]:
+            rev.add(x, f"a.cc{j}")
+    for i in act_saved:
+        rev.add(it.vars[i], f"a.cp{i}")
+    rev.run(tr.pre, names, ct_tally)
+    lines += rev.lines
+    for q, k in enumerate(wrt):
+        bid = it.bc[k].id
+        tot = f"(a.has_post ? a.pb{q} + a.cb{q} : a.cb{q})"
+        if bid in rev.ct:
+            tot = f"({tot} + {rev.ct[bid]})"
+        lines.append(f"    if (c.pv.emit({q}, {tot})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
+    lines.append("    c.trunc[item] = (fin.kc >= c.M && pred(c, fin)) ? 1 : 0;")
+    lines.append("  }")
+    lines.append("  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {")
+    lines.append(f"    ExactBins<{W}>::flush(c.pv, smem, c.gw, c.stats, tid);")
+    lines.append("  }")
+    lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int) {")
+    lines.append(f"    if (tid == 0) ExactBins<{W}>::readout(c.gw, c.g, c.stats);")
+    lines.append("  }")
+    lines.append("};")
+    lines.append("}  // namespace tmb")
+    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append("  tmb::replay_body<tmb::GenGrad, 1>(P, n);")
+    lines.append("}")
+    lines.append(f"static_assert(tmb::GenGrad::kSmemBytes == {smem_bytes}, \"shared-memory size\");")
+    return "\n".join(lines), stored_bytes, smem_bytes
+
+
+# ------------------------------------------------------------------------------------------------ programs
+def _operand(name, spec):
+    from .backend import Operand
+    if spec == "key":
+        return Operand(name, (2,), torch.int32)
+    if isinstance(spec, tuple):
+        return Operand(name, (spec[1],), TDTYPE[spec[0]])
+    return Operand(name, (), TDTYPE[spec])
+
+
+class Lowered:
+    """a traced item's programs: the forward (compiled at construction) and its reverse programs (compiled per set
+    of differentiated broadcast operands, on first use)"""
+
+    def __init__(self, fn, in_specs, n_per_item, outputs, name=None):
+        from .backend import ItemProgram, TSpec
+        self.name = name or getattr(fn, "__name__", "item")
+        specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
+        self.tr = T.trace_item(fn, in_specs, n_per_item, specs)
+        self.it = Item(self.tr, in_specs, self.name)
+        it = self.it
+        src, smem = forward_source(it)
+        self.fwd_source = src
+        pi = tuple(_operand(f"in{j}", s) for j, s in enumerate(in_specs[:n_per_item]))
+        bc = tuple(_operand(f"bc{k}", s) for k, s in enumerate(in_specs[n_per_item:]))
+        self.pi, self.bc = pi, bc
+        tallies = tuple(TSpec(nm, shape, TDTYPE[dt]) for nm, (shape, dt) in it.specs)
+        ys = tuple(_operand(f"y{r}", y.dtype) for r, y in enumerate(self.tr.results))
+        ys += (_operand("truncated", T.BOOL),)
+        nbuf = len(pi) + len(bc) + 2 + len(tallies) + 2 + len(ys)
+        kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
+        self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc, consts=("max_steps",), tallies=tallies,
+                               ys=ys, trunc=len(ys) - 1)
+        self.grads = {}
+
+    def grad_program(self, wrt):
+        """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands)"""
+        from .backend import ItemProgram, TSpec
+        wrt = tuple(wrt)
+        if wrt not in self.grads:
+            for k in wrt:
+                if self.bc[k].dtype != torch.float32:
+                    raise LowerError("tallymap_b200.lower: only float32 broadcast operands are differentiable")
+            src, stored, smem = grad_source(self.it, list(wrt))
+            fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
+            from .backend import Operand
+            bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
+            nbuf = len(self.pi) + len(bc) + 2 + 4 + 2
+            kid = compile_kernel(src, f"{self.name}_grad{''.join(map(str, wrt))}", nbuf, smem)
+            self.grads[wrt] = ItemProgram(f"{self.name}_grad", kid, pi=self.pi, bc=bc,
+                                          consts=("max_steps", "rev_checkpoints", "replay_threads"),
+                                          tallies=(TSpec("ct", (len(wrt),), exact=True),),
+                                          ys=(_operand("truncated", T.BOOL),), trunc=0,
+                                          replay_state_bytes=(stored + 3) // 4 * 4)
+        return self.grads[wrt]
+

@@ -1,0 +1,394 @@
+"""A scalar tracer for item functions: the stand-in for the jaxpr the reference's kernel backend lowers
+(tallymap/backends/kernel/kernel.py:428-451 `function()`, codegen.py:494-980 `Emitter`).
+
+An item is a Python function of (t, *per_item, *broadcast) written against `tallymap_b200.lang` (a jnp / jax.random /
+lax.while_loop / Tally.add subset).  Tracing it with placeholder values records a flat list of scalar equations, a
+jaxpr-like IR:
+
+    Eqn(prim, ins, outs, params)   ins: Var or Lit; outs: Var
+
+with dtypes f32, i32, u32 and bool.  The item must have exactly ONE top-level while loop (the reference's step
+schedule needs the same: backends/kernel/kernel.py:225-295 splits an item into pre / cond / body / post), so a traced
+item is four equation lists: `pre` (before the loop), `cond` and `body` (on the loop carry), `post` (after it).
+
+Emits (`t.add(name, index, value)`) are equations of prim "emit"; a tuple index is flattened row-major with any
+out-of-range coordinate giving -1 (tallymap/_tally.py:248-282), which the lowering drops and counts in stats[4].
+"""
+import dataclasses
+import itertools
+
+F32, I32, U32, BOOL = "f32", "i32", "u32", "bool"
+_CTX = []
+
+
+class TraceError(TypeError):
+    pass
+
+
+@dataclasses.dataclass(frozen=True)
+class Lit:
+    value: object
+    dtype: str
+
+
+@dataclasses.dataclass
+class Eqn:
+    prim: str
+    ins: list
+    outs: list
+    params: dict
+
+
+class Trace:
+    """one traced function body (a list of equations) and the variable counter it shares with nested bodies"""
+
+    def __init__(self, ids=None):
+        self.eqns = []
+        self.ids = ids if ids is not None else itertools.count()
+
+    def new(self, dtype):
+        return Var(self, next(self.ids), dtype)
+
+    def emit(self, prim, ins, out_dtypes, **params):
+        outs = [self.new(d) for d in out_dtypes]
+        self.eqns.append(Eqn(prim, list(ins), outs, params))
+        return outs
+
+
+def _cur():
+    if not _CTX:
+        raise TraceError("tallymap_b200.lang: operations on traced values outside a trace")
+    return _CTX[-1]
+
+
+def _lit(x, like=None):
+    if isinstance(x, Var):
+        return x
+    if isinstance(x, bool):
+        return Lit(bool(x), BOOL)
+    if isinstance(x, int):
+        # a Python int takes the other operand's type (a weak type, as jax's)
+        if like is not None and like.dtype == F32:
+            return Lit(float(x), F32)
+        if like is not None and like.dtype == U32:
+            return Lit(int(x) & 0xFFFFFFFF, U32)
+        return Lit(int(x), I32)
+    if isinstance(x, float):
+        if like is not None and like.dtype in (I32, U32):
+            raise TraceError("tallymap_b200.lang: a float literal combined with an integer value (use astype)")
+        return Lit(float(x), F32)
+    raise TraceError(f"tallymap_b200.lang: unsupported operand {x!r}")
+
+
+def dtype_of(x):
+    return x.dtype
+
+
+def _binary(prim, a, b, out=None):
+    a0 = a if isinstance(a, Var) else None
+    b0 = b if isinstance(b, Var) else None
+    a = _lit(a, b0)
+    b = _lit(b, a0)
+    if a.dtype != b.dtype:
+        raise TraceError(f"tallymap_b200.lang: {prim} of {a.dtype} and {b.dtype} (convert with astype)")
+    if isinstance(a, Lit) and isinstance(b, Lit):
+        raise TraceError("tallymap_b200.lang: an operation on two literals")
+    return _cur().emit(prim, [a, b], [out or a.dtype])[0]
+
+
+class Var:
+    """a traced scalar"""
+    __slots__ = ("trace", "id", "dtype")
+
+    def __init__(self, trace, id_, dtype):
+        self.trace, self.id, self.dtype = trace, id_, dtype
+
+    def __repr__(self):
+        return f"v{self.id}:{self.dtype}"
+
+    def __hash__(self):
+        return hash(self.id)
+
+    def __eq__(self, o):
+        return _binary("eq", self, o, BOOL)
+
+    def __ne__(self, o):
+        return _binary("ne", self, o, BOOL)
+
+    def __lt__(self, o):
+        return _binary("lt", self, o, BOOL)
+
+    def __le__(self, o):
+        return _binary("le", self, o, BOOL)
+
+    def __gt__(self, o):
+        return _binary("gt", self, o, BOOL)
+
+    def __ge__(self, o):
+        return _binary("ge", self, o, BOOL)
+
+    def __add__(self, o):
+        return _binary("add", self, o)
+
+    def __radd__(self, o):
+        return _binary("add", o, self)
+
+    def __sub__(self, o):
+        return _binary("sub", self, o)
+
+    def __rsub__(self, o):
+        return _binary("sub", o, self)
+
+    def __mul__(self, o):
+        return _binary("mul", self, o)
+
+    def __rmul__(self, o):
+        return _binary("mul", o, self)
+
+    def __truediv__(self, o):
+        if self.dtype != F32 and not (isinstance(o, Var) and o.dtype == F32):
+            raise TraceError("tallymap_b200.lang: '/' is float division (use // for integers)")
+        return _binary("div", self, o)
+
+    def __rtruediv__(self, o):
+        return _binary("div", o, self)
+
+    def __floordiv__(self, o):
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: // on integers only")
+        return _binary("idiv", self, o)
+
+    def __mod__(self, o):
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: % on integers only")
+        return _binary("irem", self, o)
+
+    def __neg__(self):
+        return _cur().emit("neg", [self], [self.dtype])[0]
+
+    def __and__(self, o):
+        return _binary("and", self, o)
+
+    def __rand__(self, o):
+        return _binary("and", o, self)
+
+    def __or__(self, o):
+        return _binary("or", self, o)
+
+    def __ror__(self, o):
+        return _binary("or", o, self)
+
+    def __xor__(self, o):
+        return _binary("xor", self, o)
+
+    def __invert__(self):
+        return _cur().emit("not", [self], [self.dtype])[0]
+
+    def __bool__(self):
+        raise TraceError("tallymap_b200.lang: a traced value has no Python truth value (use lang.where / while_loop)")
+
+    def astype(self, dtype):
+        dtype = _dt(dtype)
+        if dtype == self.dtype:
+            return self
+        return _cur().emit("convert", [self], [dtype])[0]
+
+
+def _dt(d):
+    from . import lang
+    m = {lang.float32: F32, lang.int32: I32, lang.uint32: U32, lang.bool_: BOOL, F32: F32, I32: I32, U32: U32,
+         BOOL: BOOL}
+    if d not in m:
+        raise TraceError(f"tallymap_b200.lang: unsupported dtype {d!r}")
+    return m[d]
+
+
+class Key:
+    """a traced PRNG key: its two uint32 words (jax.random key data)"""
+    __slots__ = ("a", "b")
+
+    def __init__(self, a, b):
+        self.a, self.b = a, b
+
+
+class TallyToken:
+    """the tally handle `t` of an item: t.add(name, index, value) records an emit and returns the handle"""
+
+    def __init__(self, specs):
+        self.specs = specs           # name -> (shape, dtype)
+
+    def add(self, name, index, value):
+        if name not in self.specs:
+            raise TraceError(f"tallymap_b200.lang: no output named {name!r} (outputs: {sorted(self.specs)})")
+        shape, dt = self.specs[name]
+        tr = _cur()
+        idx = _flat_index(index, shape)
+        v = _lit(value)
+        if isinstance(v, Lit):
+            v = Lit(float(v.value), F32) if dt == F32 else Lit(int(v.value), I32)
+        if v.dtype != dt:
+            raise TraceError(f"tallymap_b200.lang: output {name!r} sums {dt}, got {v.dtype}")
+        tr.eqns.append(Eqn("emit", [idx, v], [], dict(tally=name)))
+        return self
+
+
+def _flat_index(index, shape):
+    """row-major flat index; any coordinate outside its dimension gives -1 (_tally.py:260-271)"""
+    if not isinstance(index, tuple):
+        index = (index,)
+    if len(shape) == 0:
+        if index not in ((), (0,)):
+            raise TraceError("tallymap_b200.lang: a scalar output takes index 0 or ()")
+        return Lit(0, I32)
+    if len(index) != len(shape):
+        raise TraceError(f"tallymap_b200.lang: index of {len(index)} coordinates for an output of shape {shape}")
+    if len(index) == 1:
+        i = _lit(index[0])
+        if i.dtype != I32:
+            raise TraceError("tallymap_b200.lang: tally indices are int32")
+        return i
+    flat, ok = None, None
+    for i, n in zip(index, shape):
+        i = _lit(i)
+        if i.dtype != I32:
+            raise TraceError("tallymap_b200.lang: tally indices are int32")
+        inb = _cur().emit("inrange", [i], [BOOL], n=int(n))[0]
+        ok = inb if ok is None else (ok & inb)
+        flat = i if flat is None else flat * int(n) + i
+    return _cur().emit("select", [ok, flat, Lit(-1, I32)], [I32])[0]
+
+
+@dataclasses.dataclass
+class Traced:
+    """a traced item: pre / cond / body / post equation lists and the variables that connect them"""
+    inputs: list             # per-item operands, then broadcast ones: Var, Key, or a tuple of Vars (a vector)
+    n_per_item: int
+    pre: list
+    carry_in: list           # the loop's initial carry (Var | Lit), the tally token excluded
+    carry: list              # the carry variables as the cond / body see them
+    cond: list
+    cond_out: Var
+    body: list
+    body_out: list           # the carry after one step (Var | Lit)
+    post_carry: list         # the carry variables the post-loop code sees (the loop's final carry)
+    post: list
+    results: list            # per-item results (Var | Lit)
+    specs: dict
+
+
+class _Loop:
+    pass
+
+
+def while_loop(cond_fun, body_fun, init):
+    """the item's top-level loop (lax.while_loop); the carry is a tuple of scalars, keys and the tally handle"""
+    tr = _cur()
+    st = getattr(tr, "loop_state", None)
+    if st is None or st.get("depth", 0) != 0:
+        raise TraceError("tallymap_b200.lang: only ONE top-level while_loop per item (nested loops are not lowered)")
+    if st.get("done"):
+        raise TraceError("tallymap_b200.lang: only one top-level while_loop per item")
+    flat_in, rebuild = _flatten(init)
+    carry = []
+    body_tr = Trace(tr.ids)
+    cond_tr = Trace(tr.ids)
+    for x in flat_in:
+        if isinstance(x, TallyToken):
+            carry.append(x)
+        else:
+            v = _lit(x)
+            carry.append(body_tr.new(v.dtype))
+    # cond and body see the same carry variables
+    cvars = [c for c in carry]
+    st["depth"] = 1
+    _CTX.append(cond_tr)
+    try:
+        c = cond_fun(rebuild(cvars))
+    finally:
+        _CTX.pop()
+    if not isinstance(c, Var) or c.dtype != BOOL:
+        raise TraceError("tallymap_b200.lang: the loop condition must be a traced bool")
+    _CTX.append(body_tr)
+    try:
+        out = body_fun(rebuild(cvars))
+    finally:
+        _CTX.pop()
+    st["depth"] = 0
+    flat_out, _ = _flatten(out)
+    if len(flat_out) != len(flat_in):
+        raise TraceError("tallymap_b200.lang: the loop body must return a carry of the same structure")
+    for a, b in zip(flat_in, flat_out):
+        if isinstance(a, TallyToken) != isinstance(b, TallyToken):
+            raise TraceError("tallymap_b200.lang: the tally handle must stay in its carry position")
+    # the loop's results: fresh variables (the final carry)
+    post = [x if isinstance(x, TallyToken) else tr.new(x.dtype) for x in carry]
+    st.update(done=True, init=[x for x in flat_in], carry=cvars, cond=cond_tr.eqns, cond_out=c,
+              body=body_tr.eqns, body_out=flat_out, post_carry=post, pre_len=len(tr.eqns))
+    return rebuild(post)
+
+
+def _flatten(tree):
+    """flatten a carry (nested tuples of Var / Key / literals / TallyToken) into scalars; -> (leaves, rebuild)"""
+    leaves, spec = [], []
+
+    def go(x):
+        if isinstance(x, tuple):
+            spec.append(("tuple", len(x)))
+            for y in x:
+                go(y)
+        elif isinstance(x, Key):
+            spec.append(("key",))
+            leaves.extend([x.a, x.b])
+        else:
+            spec.append(("leaf",))
+            leaves.append(x)
+    go(tree)
+
+    def rebuild(vals):
+        it = iter(vals)
+        sp = iter(spec)
+
+        def build():
+            s = next(sp)
+            if s[0] == "tuple":
+                return tuple(build() for _ in range(s[1]))
+            if s[0] == "key":
+                return Key(next(it), next(it))
+            return next(it)
+        return build()
+    return leaves, rebuild
+
+
+def trace_item(fn, in_specs, n_per_item, specs):
+    """trace item function `fn(t, *args)`; in_specs: per argument "f32" | "i32" | "u32" | "key" | ("f32", n)
+    (a per-item vector); specs: output name -> (shape, dtype).  -> Traced"""
+    tr = Trace()
+    tr.loop_state = {"depth": 0}
+    args = []
+    for s in in_specs:
+        if s == "key":
+            args.append(Key(tr.new(U32), tr.new(U32)))
+        elif isinstance(s, tuple):
+            args.append(tuple(tr.new(s[0]) for _ in range(s[1])))
+        else:
+            args.append(tr.new(s))
+    tok = TallyToken(specs)
+    _CTX.append(tr)
+    try:
+        out = fn(tok, *args)
+    finally:
+        _CTX.pop()
+    st = tr.loop_state
+    if not st.get("done"):
+        raise TraceError("tallymap_b200.lang: the item has no while_loop (the step schedule needs one)")
+    out = out if isinstance(out, tuple) else (out,)
+    if not out or not isinstance(out[0], TallyToken):
+        raise TraceError("tallymap_b200.lang: an item returns (t, *per_item_results)")
+    results = [_lit(r) for r in out[1:]]
+    pre = tr.eqns[:st["pre_len"]]
+    post = tr.eqns[st["pre_len"]:]
+    keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
+    return Traced(inputs=args, n_per_item=n_per_item, pre=pre, carry_in=[_lit(x) for x in keep(st["init"])],
+                  carry=keep(st["carry"]), cond=st["cond"], cond_out=st["cond_out"], body=st["body"],
+                  body_out=[_lit(x) for x in keep(st["body_out"])], post_carry=keep(st["post_carry"]), post=post,
+                  results=results, specs=specs)

@@ -1,0 +1,49 @@
+"""Item functions written against tallymap_b200.lang, the traced counterparts of the hand-lowered items (the
+reference's examples/quickstart.py:19-30 walker and BASELINE config 2's walk), plus an item that exercises the other
+lowered primitives.  Shared by the lowering tests."""
+from tallymap_b200 import lang as tl
+
+
+def quickstart(t, x, key, theta):
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("hist", (x * 16).astype(tl.int32), theta * (1 - x))
+        return k + 1, x * (0.5 + 0.5 * u), t
+    k, x, t = tl.while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
+    return t, k
+
+
+def walk(t, x, key, drift):
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("hist", (x * 256).astype(tl.int32), drift * x)
+        return k + 1, x + 0.02 * (2 * u - 1), t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    t = t.add("side", (x > 1).astype(tl.int32), 1.0)
+    return t, k
+
+
+def mixer(t, pos, key, n, a, b):
+    """a fixed number of steps n (per item) so the outputs are smooth in the broadcast a and b: transcendentals,
+    select, min/max, a 3-D tuple-indexed tally, an int tally, a per-item vector"""
+    x0, y0, z0 = pos
+    def body(c):
+        k, x, y, w, t = c
+        kk = tl.random.fold_in(key, k)
+        u, v = tl.random.uniform(kk, (2,))
+        s = -tl.log(1.0 - u) / (a + b)
+        ang = 6.2831853 * v
+        x = x + s * tl.cos(ang) * tl.sqrt(w)
+        y = y + s * tl.sin(ang)
+        w = tl.where(u < 0.5, w * tl.exp(-a * s), tl.minimum(w * 1.5, tl.maximum(w, 0.25)))
+        ix = (x + 4.0).astype(tl.int32)
+        iy = (y + 4.0).astype(tl.int32)
+        iz = (k // 2) % 8
+        t = t.add("dep", (ix, iy, iz), w * tl.power(b, 0.5) + a * x * y)
+        t = t.add("hits", (k % 4,), 1)
+        return k + 1, x, y, w, t
+    k, x, y, w, t = tl.while_loop(lambda c: c[0] < n, body, (0, x0, y0 + z0, 1.0, t))
+    t = t.add("end", 0, x * a - y * b + w)
+    return t, k

@@ -1,0 +1,74 @@
+"""The lowering on the CPU: tracing item functions to the scalar IR, generating the forward and reverse ITEM
+sources, and compiling them for sm_100a with NVRTC (which needs no GPU).  Launches are in test_lower_gpu.py."""
+import numpy as np
+import pytest
+
+import tallymap_b200 as tm
+from tallymap_b200 import lang as tl
+from tallymap_b200 import lower, prng
+from tallymap_b200 import trace as T
+
+from items_lang import mixer, quickstart, walk
+
+
+def _args_walk(n=16):
+    kx, ks = prng.split(prng.PRNGKey(1), 2)
+    return prng.uniform(kx, n), prng.split(ks, n), np.float32(1.0)
+
+
+def test_trace_walk_structure():
+    tr = T.trace_item(walk, ["f32", "key", "f32"], 2, {"hist": ((256,), "f32"), "side": ((2,), "f32")})
+    assert len(tr.carry) == 2 and [v.dtype for v in tr.carry] == ["i32", "f32"]
+    assert any(e.prim == "emit" and e.params["tally"] == "hist" for e in tr.body)
+    assert any(e.prim == "emit" and e.params["tally"] == "side" for e in tr.post)
+    assert sum(e.prim == "threefry" for e in tr.body) == 1 and sum(e.prim == "uniform01" for e in tr.body) == 1
+
+
+def test_lowered_programs_compile():
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    L = f.lowered(_args_walk())
+    assert isinstance(L.fwd.kernel, int) and L.fwd.kernel > 0
+    g = L.grad_program((0,))
+    assert g.replay_state_bytes == 4          # the step counter k is the step index: only x is stored
+    assert L.it.counter == {0}
+    # the generated step VJP is the hand-lowered one's expression: ct_drift += ct_hist[bin] * x
+    src = lower.grad_source(L.it, [0])[0]
+    assert "a.cb0 = a.cb0 + g" in src
+
+
+def test_mixer_compiles_with_all_primitives():
+    kx = prng.split(prng.PRNGKey(3), 8)
+    f = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), tm.api.torch.int32),
+                                "end": tm.Sum(())},
+                in_axes=(0, 0, 0, None, None), max_steps=64)
+    pos = np.zeros((8, 3), np.float32)
+    L = f.lowered((pos, kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
+    g = L.grad_program((0, 1))
+    assert g.tallies[0].shape == (2,)
+
+
+def test_trace_errors():
+    def two_loops(t, x, key, d):
+        x = tl.while_loop(lambda c: c > 0.0, lambda c: c - 1.0, x)
+        x = tl.while_loop(lambda c: c > 0.0, lambda c: c - 1.0, x)
+        return t, x
+    with pytest.raises(T.TraceError, match="one top-level"):
+        T.trace_item(two_loops, ["f32", "key", "f32"], 2, {})
+
+    def no_loop(t, x, key, d):
+        return t, x
+    with pytest.raises(T.TraceError, match="no while_loop"):
+        T.trace_item(no_loop, ["f32", "key", "f32"], 2, {})
+
+    def mixed(t, x, key, d):
+        def body(c):
+            return c + (c > 0.0).astype(tl.int32)
+        x = tl.while_loop(lambda c: c > 0.0, body, x)
+        return t, x
+    with pytest.raises(T.TraceError, match="convert"):
+        T.trace_item(mixed, ["f32", "key", "f32"], 2, {})
+
+
+def test_compile_error_reports_nvrtc_log(tmlib):
+    with pytest.raises(tmlib.TallymapError, match="NVRTC failed"):
+        lower.compile_kernel("this is not CUDA", "broken", 3, 16)

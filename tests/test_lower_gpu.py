@@ -1,0 +1,119 @@
+"""GPU parity of run-time lowered items (tallymap_b200.trace -> lower -> NVRTC): the traced quickstart walker and
+1-D walk against the oracle and against the hand-lowered kernels -- trip counts, flags, stats and gradients bitwise,
+float tallies within the float-tally tolerance -- and an item using the other lowered primitives, whose generated
+gradient is checked against a central difference of its generated forward."""
+import numpy as np
+import pytest
+import torch
+
+import tallymap_b200 as tm
+from tallymap_b200 import backend as B
+from tallymap_b200 import prng
+
+from items_lang import mixer, quickstart, walk
+
+pytestmark = pytest.mark.gpu
+FT = 1e-5
+
+
+def near(a, b, tol=FT):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return np.abs(a - b).max() <= tol * max(np.abs(b).max(), 1e-30)
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def rw_inputs(n, seed=1):
+    kx, ks = prng.split(prng.PRNGKey(seed), 2)
+    return prng.uniform(kx, n), prng.split(ks, n)
+
+
+def np_out(r):
+    return {k: v.cpu().numpy() for k, v in r.outputs.items()}
+
+
+@pytest.mark.parametrize("n", [1, 3000, 65536])
+def test_lowered_walk_forward(cuda, orc, n):
+    x, k = rw_inputs(n, seed=2)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    r = f(x, k, np.float32(1.0))
+    torch.cuda.synchronize()
+    ref = orc.rw_fwd(x, k, 1.0)
+    assert np.array_equal(r.per_item.cpu().numpy(), ref["k"])
+    assert np.array_equal(r.truncated.cpu().numpy(), ref["trunc"])
+    st = np.array([int(r.stats[s]) for s in B.STATS])
+    assert np.array_equal(st, ref["stats"])
+    o = np_out(r)
+    if not ref["trunc"].any():
+        assert near(o["hist"], ref["hist"]) and near(o["side"], ref["side"])
+    hand = B.run(B.RW_FWD, [x, k], [np.float32(1.0)], consts=(20000,))
+    assert np.array_equal(hand[3].cpu().numpy(), ref["k"])
+
+
+@pytest.mark.parametrize("C", [None, 3])
+def test_lowered_walk_grad_bitwise(cuda, orc, C):
+    x, k = rw_inputs(20000, seed=3)
+    ct = np.random.default_rng(4).normal(size=256).astype(np.float32)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    prog = f.lowered((x, k, np.float32(1.0))).grad_program((0,))
+    out = B.run(prog, [x, k], [np.float32(1.0), ct, np.zeros(2, np.float32)], consts=(20000,), rev_checkpoints=C)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    g = out[0].cpu().numpy()
+    ref = orc.rw_grad(x, k, 1.0, ct)
+    hand = B.run(B.RW_GRAD, [x, k], [np.float32(1.0), ct, np.zeros(2, np.float32)], consts=(20000,))
+    assert np.array_equal(bits(g), bits(ref["g"]))
+    assert np.array_equal(bits(g), bits(hand[0].cpu().numpy()))
+    # and through the API
+    gg = f.grad(x, k, np.float32(1.0), wrt=2, cotangents={"hist": ct})
+    assert np.array_equal(bits(gg.cpu().numpy().reshape(1)), bits(ref["g"]))
+
+
+def test_lowered_quickstart(cuda, orc):
+    x = np.linspace(0.1, 0.99, 10000, dtype=np.float32)
+    k = prng.split(prng.PRNGKey(0), 10000)
+    f = tm.vmap(quickstart, outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=100)
+    r, g = f.value_and_grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": np.ones(16, np.float32)})
+    torch.cuda.synchronize()
+    rf = orc.q1_fwd(x, k, 2.0)
+    rg = orc.q1_grad(x, k, 2.0, np.ones(16, np.float32))
+    assert np.array_equal(r.per_item.cpu().numpy(), rf["k"])
+    assert near(np_out(r)["hist"], rf["hist"])
+    assert np.array_equal(bits(g.cpu().numpy().reshape(1)), bits(rg["g"]))
+
+
+def _mixer_args(n, a, b):
+    keys = prng.split(prng.PRNGKey(8), n)
+    rng = np.random.default_rng(1)
+    pos = (0.3 * rng.standard_normal((n, 3))).astype(np.float32)
+    steps = rng.integers(1, 7, n).astype(np.int32)
+    return pos, keys, steps, np.float32(a), np.float32(b)
+
+
+def test_lowered_mixer_forward_and_gradient(cuda):
+    n = 4000
+    outs = {"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), torch.int32), "end": tm.Sum(())}
+    f = tm.vmap(mixer, outputs=outs, in_axes=(0, 0, 0, None, None), max_steps=64)
+    args = _mixer_args(n, 0.3, 1.7)
+    r1, r2 = f(*args), f(*args)
+    torch.cuda.synchronize()
+    # the int tally is exact: item i adds 1 to bin s % 4 for s < steps[i]
+    steps = args[2]
+    want = np.zeros(4, np.int64)
+    for s in range(int(steps.max())):
+        want[s % 4] += int((steps > s).sum())
+    assert np.array_equal(r1.outputs["hits"].cpu().numpy(), want)
+    assert np.array_equal(r1.per_item.cpu().numpy(), steps)
+    assert near(r1.outputs["dep"].cpu().numpy(), r2.outputs["dep"].cpu().numpy(), 1e-6)
+    # gradient of <1, dep> + 0.5 end w.r.t. (a, b) against a central difference of the forward (f64 sums)
+    cts = {"dep": np.ones((8, 8, 8), np.float32), "end": np.float32(0.5)}
+    g = f.grad(*args, wrt=(3, 4), cotangents=cts).cpu().numpy()
+
+    def loss(a, b):
+        r = f(*_mixer_args(n, a, b))
+        return float(r.outputs["dep"].double().sum()) + 0.5 * float(r.outputs["end"].double().sum())
+    for j, (a, b) in enumerate([(1e-3, 0.0), (0.0, 1e-3)]):
+        fd = (loss(0.3 + a, 1.7 + b) - loss(0.3 - a, 1.7 - b)) / 2e-3
+        assert abs(g[j] - fd) <= 2e-2 * abs(fd) + 1e-2, (j, g[j], fd)
