@@ -262,11 +262,20 @@ def replay_plan(p, max_steps, rev_checkpoints=None, device=None):
 
 
 def replay_scratch_states(C, max_steps, pipelined=False):
-    """compact states per thread of the replay scratch: the head alone when C >= max_steps (two heads for a pipelined
-    value-and-grad kernel), else head + checkpoints + tape (the replay kernel's layout)"""
+    """compact states per thread of the replay scratch: the head alone when C >= max_steps (for a pipelined
+    value-and-grad kernel: its ring tape of C + 1 states), else head + checkpoints + tape (the replay kernel's
+    layout)"""
     if C >= max_steps:
-        return 2 * (C + 1) if pipelined else C + 1
+        return C + 1
     return 3 * C + 1
+
+
+def ring_states(max_steps):
+    """the ring tape of a pipelined value-and-grad kernel: the smallest power of two >= max_steps + 2 states"""
+    T = 1
+    while T < int(max_steps) + 2:
+        T *= 2
+    return T
 
 
 def _replay_plan(p, max_steps, rev_checkpoints, device):
@@ -282,8 +291,10 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
     else:
         free, _ = torch.cuda.mem_get_info(device)
         budget = REV_BUDGET_FRACTION * free
-        if M <= 2 ** 30 and threads * per(M) <= budget:
-            C = max(M, 1)
+        pipelined = p.vg_fallback is not None
+        Ch = ring_states(M) - 1 if pipelined and M <= 2 ** 29 else M
+        if M <= 2 ** 29 and threads * per(Ch) <= budget:
+            C = max(Ch, 1)
         else:
             C = REV_C_MIN
             while C * 2 < M and C * 2 <= REV_C_POW2_MAX and threads * per(C * 2) <= budget:
@@ -341,7 +352,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
     kernel = p.kernel
-    if p.vg_fallback is not None and known["rev_checkpoints"] < known["max_steps"]:
+    if p.vg_fallback is not None and (known["rev_checkpoints"] + 1 != ring_states(known["max_steps"])):
         kernel = p.vg_fallback          # (items may outgrow the head: the fused replay's checkpointed schedule)
     kid, nbuf = kernel_ref(kernel)
     ptrs = [0 if t is None else t.data_ptr() for t in args] + [t.data_ptr() for t in res]
