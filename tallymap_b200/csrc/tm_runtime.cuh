@@ -312,18 +312,19 @@ __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const 
 }
 
 // ------------------------------------------------------------------------------------------------ pipelined value and grad
-// vg_kernel<I, V>: a fused value-and-grad program (I::kFused) when every item fits the head (C >= max_steps).  In the
-// replay kernel a lane counts an item, then sweeps it, so at any iteration some lanes of a warp count and others
-// sweep and the warp pays for both paths.  Here each lane pipelines two items through two head buffers: it counts
-// item n (one forward step with emits per iteration, storing the states) while it sweeps item n - 1 (up to V step
-// VJPs per iteration, newest first) from the other buffer.  Every iteration then runs the forward step for (nearly)
-// every lane; a lane whose count ends before its previous sweep does waits, sweeping, until the sweep is done.  The
-// step VJPs of an item run in the replay's order on the same states, so the gradient is bitwise the replay's.
-// Scratch: 2 (C + 1) states per thread.  ITEM additions: handoff(Ctx& sweep, const Ctx& count) gives the sweeping
-// context an item's per-item context while keeping its own per-thread accumulators.
+// vg_kernel<I, V>: a fused value-and-grad program (I::kFused) when every item fits the scratch (C >= max_steps).
+// In the replay kernel a lane counts an item, then sweeps it, so at any iteration some lanes of a warp count and
+// others sweep and the warp pays for both paths.  Here each lane keeps a ring tape of T = C + 1 stored states
+// (T a power of two >= max_steps + 2): it counts items back to back into the tape -- one forward step with emits per
+// iteration, each item followed by its final state -- while it sweeps the oldest counted item, newest state first,
+// one step VJP per iteration (up to V when it has nothing left to count).  So the forward step and one VJP run for
+// nearly every lane every iteration.  A lane whose tape or queue of counted items is full waits (sweeping) before
+// it counts on.  The step VJPs of an item run in the replay's order on the same states: the gradient is bitwise the
+// replay's.  ITEM additions: restore() of an item's final state at step K.
 template <class I, int V>
 __device__ __forceinline__ void vg_body(const Params& P, const i64 n_items) {
   static_assert(fused_trait<I>::value, "vg_kernel runs fused value-and-grad programs");
+  constexpr int kQ = 8;             // counted items awaiting their sweep, per lane
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
   I::setup(cx, P, smem);
@@ -340,33 +341,34 @@ __device__ __forceinline__ void vg_body(const Params& P, const i64 n_items) {
   const i64 gtid = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   typedef typename I::Stored S;
   typedef typename I::State X;
-  // the host launches this kernel only with C >= max_steps; a thread beyond the planned scratch, or a launch that
-  // breaks that rule, takes no items and sets the error word (bit 1)
-  const bool have = gtid < cap && C >= 1 && C >= __ldg(&consts[I::kConstM]);
+  const u32 T = (u32)C + 1u, mask = T - 1u;
+  // the host launches this kernel only with T a power of two >= max_steps + 2; a thread beyond the planned scratch,
+  // or a launch that breaks that rule, takes no items and sets the error word (bit 1)
+  const bool have = gtid < cap && C >= 1 && (T & mask) == 0u && (i64)T >= (i64)__ldg(&consts[I::kConstM]) + 2;
   if (!have) atomicOr(&ctl[kCtlError], 2u);
-  S* const buf = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * 2 * ((i64)C + 1);
-  typename I::Ctx cs = cx;          // the sweeping item's context
-  X x, xinit, sinit, sfin;
+  S* const tape = static_cast<S*>(P.p[I::kReplay]) + (have ? gtid : 0) * (i64)T;
+  typename I::Ctx cs = cx;          // the sweeping item's context (its per-item fields, the thread's accumulators)
+  X x, sinit, sfin;
   typename I::Adj adj;
   i64 item = 0, sitem = 0;
-  i32 k = 0, si = -1;               // si >= 0: the sweep's next state index
-  int cb = 0, sb = 1;               // the buffers of the counting and the sweeping item
-  bool counting = false, alive = have;
+  i32 k = 0, si = -1, sK = 0;
+  u32 wpos = 0u, rlo = 0u, cstart = 0u, sstart = 0u;   // tape positions (mod 2^32; the tape index is pos & mask)
+  i64 q_item[kQ];
+  i32 q_k[kQ];
+  u32 q_start[kQ];
+  u32 qh = 0u, qt = 0u;
+  bool counting = false, sweeping = false, alive = have;
   for (;;) {
     bool c_ok = counting && I::cond(cx, x);
-    if (counting && !c_ok && si < 0) {
-      // the count pass ended: the forward's post-loop code, then the item moves to the sweep slot
+    if (counting && !c_ok && qt - qh < (u32)kQ && wpos - rlo < T) {
+      // the count pass ended: the forward's post-loop code; the final state follows the item's states on the tape
       I::fwd_finish(cx, x, item);
-      I::handoff(cs, cx);
-      sinit = xinit;
-      sfin = x;
-      sitem = item;
-      sb = cb;
-      cb ^= 1;
-      I::adj_start(cs, adj);
-      I::post_vjp(cs, sfin, adj);
-      si = k - 1;
-      if (si < 0) I::adj_finish(cs, sinit, sfin, adj, sitem);
+      tape[wpos & mask] = I::store(x);
+      ++wpos;
+      q_item[qt % kQ] = item;
+      q_k[qt % kQ] = k;
+      q_start[qt % kQ] = cstart;
+      ++qt;
       counting = false;
     }
     if (alive && !counting) {
@@ -376,30 +378,49 @@ __device__ __forceinline__ void vg_body(const Params& P, const i64 n_items) {
       } else {
         item = ticket_item(order, t);
         x = I::start(cx, item);
-        xinit = x;
         k = 0;
+        cstart = wpos;
         counting = true;
         c_ok = I::cond(cx, x);
       }
     }
-    if (!__any_sync(0xffffffffu, counting || si >= 0)) break;
+    if (!sweeping && qh != qt) {
+      sitem = q_item[qh % kQ];
+      sK = q_k[qh % kQ];
+      sstart = q_start[qh % kQ];
+      ++qh;
+      sinit = I::start(cs, sitem);     // (re-derives the item's per-item context; the accumulators stay)
+      sfin = I::restore(cs, tape[(sstart + (u32)sK) & mask], sK);
+      I::adj_start(cs, adj);
+      I::post_vjp(cs, sfin, adj);
+      si = sK - 1;
+      sweeping = true;
+    }
+    if (!__any_sync(0xffffffffu, counting || sweeping || alive)) break;
+    // a step needs its slot and one more for the item's final state
+    const bool step_now = c_ok && (wpos - rlo + 2u <= T);
     __syncwarp();
-    if (c_ok) {
-      buf[cb * ((i64)C + 1) + k] = I::store(x);
+    if (step_now) {
+      tape[wpos & mask] = I::store(x);
+      ++wpos;
       ++k;
       I::fwd_emit(cx, x, true);
     }
     __syncwarp();
-    if (si >= 0) {
-      const S* const src = buf + sb * ((i64)C + 1);
-      S st[V];
+    if (sweeping) {
+      const int nv = counting ? 1 : V;
 #pragma unroll
-      for (int v = 0; v < V; ++v) st[v] = src[si - v >= 0 ? si - v : 0];
-#pragma unroll
-      for (int v = 0; v < V; ++v)
-        if (si - v >= 0) I::vjp(cs, I::restore(cs, st[v], si - v), adj);
-      si -= V;
-      if (si < 0) I::adj_finish(cs, sinit, sfin, adj, sitem);
+      for (int v = 0; v < V; ++v) {
+        if (v < nv && si >= 0) {
+          I::vjp(cs, I::restore(cs, tape[(sstart + (u32)si) & mask], si), adj);
+          --si;
+        }
+      }
+      if (si < 0) {
+        I::adj_finish(cs, sinit, sfin, adj, sitem);
+        rlo = sstart + (u32)sK + 1u;
+        sweeping = false;
+      }
     }
   }
   __syncthreads();
