@@ -289,6 +289,7 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
         if C < 1:
             raise ValueError("tallymap_b200: rev_checkpoints must be >= 1")
     else:
+        torch.cuda.empty_cache()             # (blocks cached by earlier calls count as free)
         free, _ = torch.cuda.mem_get_info(device)
         budget = REV_BUDGET_FRACTION * free
         pipelined = p.vg_fallback is not None
@@ -390,6 +391,7 @@ def record_capacity(N, record=None, device=None):
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     key = (int(N), dev.index)
     if key not in _RECORD:
+        torch.cuda.empty_cache()             # (blocks cached by earlier calls count as free)
         free, _ = torch.cuda.mem_get_info(dev)
         _RECORD[key] = int(max(1, min(2 ** 31 - 1, max(RECORD_MIN, RECORD_PER_ROOT * int(N)),
                                       RECORD_BUDGET_FRACTION * free // RECORD_SLOT_BYTES)))
@@ -414,14 +416,27 @@ def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_che
     import ctypes
     dev = torch.device("cuda", torch.cuda.current_device())
     st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
-    fwd = run(SH_REC, pi, [X0], consts=(max_steps,), queue=queue, record=record, stream=st)
-    last = run.last
-    res, args = last["results"], last["args"]
-    R = int(last["consts"][SH_REC.consts.index("record")])
-    N = int(args[0].shape[0])
-    rec, root_last, stats = res["record"], res["last"], res["stats"]
-    head = torch.cat([res["tree"][:1], stats.to(torch.int64)]).cpu()        # (one sync)
-    total, dropped = int(head[0]), int(head[1 + STATS.index("children_dropped")])
+    for attempt in range(2):
+        fwd = run(SH_REC, pi, [X0], consts=(max_steps,), queue=queue, record=record, stream=st)
+        last = run.last
+        res, args = last["results"], last["args"]
+        R = int(last["consts"][SH_REC.consts.index("record")])
+        N = int(args[0].shape[0])
+        rec, root_last, stats = res["record"], res["last"], res["stats"]
+        head = torch.cat([res["tree"][:1], stats.to(torch.int64)]).cpu()        # (one sync)
+        total, dropped = int(head[0]), int(head[1 + STATS.index("children_dropped")])
+        if total <= R or record is not None or attempt == 1 or total >= 2 ** 31:
+            break
+        # the default capacity was short: the recording is deterministic, so record again with exactly the children
+        # it counted, when they fit beside what is allocated (and keep that capacity for later calls with N roots)
+        free, _ = torch.cuda.mem_get_info(dev)
+        if total * RECORD_SLOT_BYTES > 0.9 * (free + rec.numel() * rec.element_size()):
+            break
+        del fwd, last, res, rec, root_last, stats
+        run.last = None
+        torch.cuda.empty_cache()
+        _RECORD[(N, dev.index)] = total
+        record = total
     n_rec = min(total, R)
     L = _lib.lib()
     counts = torch.empty(TREE_MAX_GEN + 1, dtype=torch.int64, device=dev)
