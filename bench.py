@@ -44,8 +44,9 @@ METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per item of one launch, from the ncu captures summarised
 # under profiles/ (kernel -> (bytes per item, items in the capture)); the bench scales them to its own launch
 TRAFFIC = {
+    "rw_vg": ((38916657408 + 37082540288) / 4194304, 4194304),
     "rw_grad": ((5.241173e9 + 6.034955e9) / 1048576, 1048576),
-    "rw_fwd": ((52.543232e6 + 4.872960e6) / 4194304, 4194304),
+    "rw_fwd": ((53075712 + 3524096) / 4194304, 4194304),
     "ph_fwd": ((10.557440e6 + 0.0) / 1048576, 1048576),
 }
 
