@@ -23,12 +23,18 @@ from . import backend as B
 
 @dataclasses.dataclass(frozen=True)
 class Sum:
-    """a summed output of a fixed shape (tallymap.Sum, _api.py:55-84)."""
+    """a summed output of a fixed shape (tallymap.Sum, _api.py:55-84).  fixed_point=True (float32, items traced from
+    Python functions): EXACT -- each bin is the correctly rounded float32 of the exact sum of its emits, bitwise
+    independent of their order (run to run, launch order, number of GPUs); a non-finite emit or an accumulator
+    overflow makes the bin NaN, counted in stats['fixed_point_overflow']."""
     shape: tuple
     dtype: torch.dtype = torch.float32
+    fixed_point: bool = False
 
     def __post_init__(self):
         object.__setattr__(self, "shape", tuple(int(s) for s in self.shape))
+        if self.fixed_point and self.dtype != torch.float32:
+            raise NotImplementedError("tallymap_b200: fixed_point Sums of float32 only (the exact accumulator)")
 
 
 class Result(NamedTuple):
@@ -235,7 +241,8 @@ class MappedFn:
         for name, o in outputs.items():
             if o.dtype not in (torch.float32, torch.int32):
                 raise TypeError(f"tallymap_b200: output {name!r}: Sum of float32 or int32")
-            self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32")
+            self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32",
+                                  bool(getattr(o, "fixed_point", False)))
         self.in_axes = tuple(in_axes)
         if any(ax not in (0, None) for ax in self.in_axes):
             raise ValueError("tallymap_b200: in_axes entries are 0 (per item) or None (broadcast)")
@@ -316,7 +323,7 @@ class MappedFn:
         pi, bc = self._split(args)
         n = int((pi[0] if isinstance(pi[0], torch.Tensor) else B._host(pi[0])).shape[0]) if pi else 0
         cts = []
-        for name, (shape, dt) in self.outputs.items():
+        for name, (shape, dt, _) in self.outputs.items():
             if dt != "f32":
                 continue
             c = cotangents.get(name)

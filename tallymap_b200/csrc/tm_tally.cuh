@@ -45,6 +45,68 @@ struct ExactBins {
   }
 };
 
+// ------------------------------------------------------------------------------------------------ fixed-point Sums
+// A Sum(fixed_point=True) of f32 (tallymap/_api.py:55-84; kernel.py:870-941): every emit is added exactly into its
+// bin's carry-save words (atomics, on shared or global words), so the bin is the correctly rounded f32 of the exact
+// sum whatever the order of the emits.  A non-finite emit or a carry out of the top word flags the bin (NaN at
+// readout), counted in stats[3]; an index outside [0, S) is dropped and counted in stats[4].
+__device__ __forceinline__ bool exact_emit_atomic(u64* w, float v) {
+  const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
+  if (e == 255u) return true;
+  const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
+  if (m == 0ull) return false;
+  const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
+  const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
+  const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;   // (s >= 40 only for j <= 3: j + 1 is a word)
+  const bool neg = (bits >> 31) != 0u;
+  bool lost = false;
+  if (lo) lost = exact_add_word(w, (int)j, neg ? -lo : lo);
+  if (hi) lost = exact_add_word(w, (int)j + 1, neg ? -hi : hi) || lost;
+  return lost;
+}
+
+template <int S>
+struct ExactSum {
+  // words: S x 5 u64, then S u32 flags (shared or global); bytes of that layout
+  static constexpr int kBytes = S * kExactWords * 8 + S * 4;
+  __device__ __forceinline__ static void emit(u64* words, i32* stats, i32 b, float v) {
+    if ((u32)b >= (u32)S) {
+      atomicAdd(&stats[kStDroppedEmits], 1);
+      return;
+    }
+    if (exact_emit_atomic(words + (i64)b * kExactWords, v)) {
+      atomicOr(reinterpret_cast<u32*>(words + (i64)S * kExactWords) + b, 1u);
+      atomicAdd(&stats[kStFixedPointOverflow], 1);
+    }
+  }
+  // a block's shared words into the launch's global words (global flags packed after the words, as ExactBins)
+  __device__ static void flush(const u64* sw, u64* gw, i32* stats, int tid, int nth) {
+    const u32* const sf = reinterpret_cast<const u32*>(sw + (i64)S * kExactWords);
+    u32* const gf = reinterpret_cast<u32*>(gw + (i64)S * kExactWords);
+    for (int b = tid; b < S; b += nth) {
+      i64 wv[kExactWords];
+      bool any = false;
+      for (int j = 0; j < kExactWords; ++j) {
+        wv[j] = (i64)sw[b * kExactWords + j];
+        any = any || wv[j] != 0;
+      }
+      const bool lost = any && exact_merge_bin(gw + (i64)b * kExactWords, wv);
+      if (lost) atomicAdd(&stats[kStFixedPointOverflow], 1);
+      if (lost || sf[b]) atomicOr(&gf[b], 1u);
+    }
+  }
+  // global words -> the f32 output (the last block, all its threads)
+  __device__ static void readout(const u64* gw, float* out, i32* stats, int tid, int nth) {
+    const u32* const gf = reinterpret_cast<const u32*>(gw + (i64)S * kExactWords);
+    for (int b = tid; b < S; b += nth) {
+      bool bad = false;
+      const float o = exact_read(gw + (i64)b * kExactWords, &bad);
+      if (bad && !gf[b]) atomicAdd(&stats[kStFixedPointOverflow], 1);
+      out[b] = (gf[b] || bad) ? __int_as_float(0x7fc00000) : o;
+    }
+  }
+};
+
 // An f32 sum tally in global memory, accumulated in an f64 shadow and warp-aggregated.  The lanes of a warp that add
 // into the same bin in this call (found with __match_any_sync) sum their values in f64 in ascending lane order, and
 // the lowest lane issues one f64 atomic add; the epilogue rounds every bin once to f32 (f64_to_f32).

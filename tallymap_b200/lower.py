@@ -163,8 +163,9 @@ def _defs(eqns):
 class Item:
     """the layout facts of a traced item shared by its forward and reverse lowering"""
 
-    def __init__(self, tr, in_specs, name):
+    def __init__(self, tr, in_specs, name, exact=()):
         self.tr, self.name = tr, name
+        self.exact = set(exact)                 # Sum(fixed_point=True) f32 outputs: exact bins
         self.in_specs = list(in_specs)
         npi = tr.n_per_item
         self.pi, self.bc = tr.inputs[:npi], tr.inputs[npi:]
@@ -264,6 +265,9 @@ def forward_source(it):
     enum.append(f"kOrder = {idx}"); idx += 1
     for t, _ in enumerate(it.specs):
         enum.append(f"kT{t} = {idx}"); idx += 1
+    for t, (name, _) in enumerate(it.specs):
+        if name in it.exact:
+            enum.append(f"kX{t} = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
@@ -275,9 +279,10 @@ def forward_source(it):
     smem, priv = 0, {}
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
-        if S * 4 <= PRIV_BYTES:
+        nbytes = S * 44 if name in it.exact else S * 4
+        if nbytes <= (4 * PRIV_BYTES if name in it.exact else PRIV_BYTES):
             priv[name] = (t, smem, S, dt)
-            smem += S * 4
+            smem += (nbytes + 15) // 16 * 16
     lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
     # context
     ctx = ["  struct Ctx {"]
@@ -292,7 +297,11 @@ def forward_source(it):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
         ct = "float" if dt == T.F32 else "i32"
         ctx.append(f"    {ct}* g{t};")
-        if name in priv:
+        if name in it.exact:
+            ctx.append(f"    u64* x{t};")
+            if name in priv:
+                ctx.append(f"    u64* sx{t};")
+        elif name in priv:
             ctx.append(f"    {ct}* s{t};")
         tinfo[name] = (t, S, dt, name in priv)
     for r, y in enumerate(tr.results):
@@ -318,7 +327,11 @@ def forward_source(it):
     for name, (t, S, dt, pv) in tinfo.items():
         ct = "float" if dt == T.F32 else "i32"
         lines.append(f"    c.g{t} = static_cast<{ct}*>(P.p[kT{t}]);")
-        if pv:
+        if name in it.exact:
+            lines.append(f"    c.x{t} = static_cast<u64*>(P.p[kX{t}]);")
+            if pv:
+                lines.append(f"    c.sx{t} = reinterpret_cast<u64*>(smem + {priv[name][1]});")
+        elif pv:
             lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[name][1]});")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
@@ -328,6 +341,8 @@ def forward_source(it):
 
     def emitter(name, idx_c, v_c):
         t, S, dt, pv = tinfo[name]
+        if name in it.exact:
+            return f"ExactSum<{S}>::emit({'c.sx' if pv else 'c.x'}{t}, c.stats, {idx_c}, {v_c});"
         if dt == T.F32:
             if pv:
                 return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
@@ -371,12 +386,18 @@ def forward_source(it):
     for name, (t, S, dt, pv) in tinfo.items():
         if not pv:
             continue
-        if dt == T.F32:
+        if name in it.exact:
+            lines.append(f"    ExactSum<{S}>::flush(c.sx{t}, c.x{t}, c.stats, tid, nth);")
+        elif dt == T.F32:
             lines.append(f"    SumPriv<{S}>::flush(c.s{t}, c.g{t}, tid, nth);")
         else:
             lines.append(f"    for (int b = tid; b < {S}; b += nth) if (c.s{t}[b]) atomicAdd(&c.g{t}[b], c.s{t}[b]);")
     lines.append("  }")
-    lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
+    lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int nth) {")
+    for name, (t, S, dt, pv) in tinfo.items():
+        if name in it.exact:
+            lines.append(f"    ExactSum<{S}>::readout(c.x{t}, c.g{t}, c.stats, tid, nth);")
+    lines.append("  }")
     lines.append("};")
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
@@ -785,18 +806,19 @@ class Lowered:
         from .backend import ItemProgram, TSpec
         self.name = name or getattr(fn, "__name__", "item")
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
+        exact = [k for k, v in outputs.items() if len(v) > 2 and v[2]]
         self.tr = T.trace_item(fn, in_specs, n_per_item, specs)
-        self.it = Item(self.tr, in_specs, self.name)
+        self.it = Item(self.tr, in_specs, self.name, exact)
         it = self.it
         src, smem = forward_source(it)
         self.fwd_source = src
         pi = tuple(_operand(f"in{j}", s) for j, s in enumerate(in_specs[:n_per_item]))
         bc = tuple(_operand(f"bc{k}", s) for k, s in enumerate(in_specs[n_per_item:]))
         self.pi, self.bc = pi, bc
-        tallies = tuple(TSpec(nm, shape, TDTYPE[dt]) for nm, (shape, dt) in it.specs)
+        tallies = tuple(TSpec(nm, shape, TDTYPE[dt], exact=nm in it.exact) for nm, (shape, dt) in it.specs)
         ys = tuple(_operand(f"y{r}", y.dtype) for r, y in enumerate(self.tr.results))
         ys += (_operand("truncated", T.BOOL),)
-        nbuf = len(pi) + len(bc) + 2 + len(tallies) + 2 + len(ys)
+        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + 2 + len(ys)
         kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc, consts=("max_steps",), tallies=tallies,
                                ys=ys, trunc=len(ys) - 1)

@@ -72,3 +72,13 @@ def test_trace_errors():
 def test_compile_error_reports_nvrtc_log(tmlib):
     with pytest.raises(tmlib.TallymapError, match="NVRTC failed"):
         lower.compile_kernel("this is not CUDA", "broken", 3, 16)
+
+
+def test_fixed_point_sum_lowers_to_exact_bins():
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,), fixed_point=True), "side": tm.Sum((2,))},
+                in_axes=(0, 0, None), max_steps=20000)
+    L = f.lowered(_args_walk())
+    assert [t.exact for t in L.fwd.tallies] == [True, False]
+    assert "ExactSum<256>::emit(c.sx0" in L.fwd_source and "ExactSum<256>::readout" in L.fwd_source
+    with pytest.raises(NotImplementedError):
+        tm.Sum((4,), tm.api.torch.int32, fixed_point=True)

@@ -117,3 +117,28 @@ def test_lowered_mixer_forward_and_gradient(cuda):
     for j, (a, b) in enumerate([(1e-3, 0.0), (0.0, 1e-3)]):
         fd = (loss(0.3 + a, 1.7 + b) - loss(0.3 - a, 1.7 - b)) / 2e-3
         assert abs(g[j] - fd) <= 2e-2 * abs(fd) + 1e-2, (j, g[j], fd)
+
+
+def test_fixed_point_sums_are_order_independent(cuda, orc):
+    """Sum(fixed_point=True): bitwise the same under any claim order, within one ulp of the oracle's f64 sums
+    (the correctly rounded exact sum), while the plain f32 side tally is only within tolerance"""
+    n = 200000
+    x, k = rw_inputs(n, seed=6)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,), fixed_point=True), "side": tm.Sum((2,), fixed_point=True)},
+                in_axes=(0, 0, None), max_steps=20000)
+    L = f.lowered((x, k, np.float32(1.0)))
+    outs = []
+    for order in (None, np.arange(n, dtype=np.int32)[::-1].copy(),
+                  np.random.default_rng(1).permutation(n).astype(np.int32)):
+        o = B.run(L.fwd, [x, k], [np.float32(1.0)], consts=(20000,), order=order)
+        torch.cuda.synchronize()
+        B.check_status(B.run.last["ctl"])
+        outs.append([t.cpu().numpy() for t in o])
+    for o in outs[1:]:
+        assert np.array_equal(bits(o[0]), bits(outs[0][0])) and np.array_equal(bits(o[1]), bits(outs[0][1]))
+        assert np.array_equal(o[3], outs[0][3])
+    ref = orc.rw_fwd(x, k, 1.0)          # f64 partial sums, rounded once
+    h = outs[0][0]
+    ulps = np.abs(h.view(np.int32).astype(np.int64) - ref["hist"].view(np.int32).astype(np.int64))
+    assert ulps.max() <= 1 and (ulps == 0).mean() > 0.99
+    assert np.array_equal(outs[0][1], ref["side"])
