@@ -16,6 +16,7 @@ program family rather than traced from a Python function.
 import dataclasses
 from typing import Any, NamedTuple
 
+import numpy as np
 import torch
 
 from . import backend as B
@@ -333,6 +334,51 @@ class MappedFn:
         trunc = out[2]
         ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
         return ct.reshape(()) if isinstance(wrt, int) else ct
+
+    def jvp(self, *args, wrt, tangents):
+        """forward mode (tallymap's jvp of a mapped call, _api.py:305-345): ONE launch of the generated tangent program.
+        wrt: float32 broadcast argument index or tuple of W indices; tangents: W values (one tangent lane) or an
+        array [L, W] (L <= 16 lanes, the reference's dual lanes).  -> (Result, {output name: tangent}), a tangent of
+        shape (*output.shape) for one lane, (L, *output.shape) for L lanes; NaN when an item hit max_steps."""
+        from . import lower
+        L_ = self.lowered(args)
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if any(self.in_axes[w] is not None for w in idx):
+            raise ValueError("tallymap_b200: tangents of per-item operands are not lowered")
+        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
+        tan = torch.as_tensor(np.asarray(tangents, np.float32) if not isinstance(tangents, torch.Tensor)
+                              else tangents, dtype=torch.float32)
+        lanes_given = tan.dim() == 2
+        tan = tan.reshape(-1, len(idx))
+        L = int(tan.shape[0])
+        if L > lower.LANES_MAX:
+            raise ValueError(f"tallymap_b200: at most {lower.LANES_MAX} tangent lanes per launch")
+        prog = L_.jvp_program(bpos, L)
+        pi, bc = self._split(args)
+        out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,))
+        nf = len(L_.fwd.tallies)
+        nt = len(prog.tallies)
+        tallies = {t.name: v for t, v in zip(prog.tallies[:nf], out[:nf])}
+        dts = {t.name[2:]: v for t, v in zip(prog.tallies[nf:], out[nf:nt])}
+        stats_raw = out[nt]
+        ys = out[nt + 1:]
+        trunc = ys[prog.trunc].bool()
+        per = [y for i, y in enumerate(ys) if i != prog.trunc]
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        res = Result(_poison(tallies, n_tr > 0), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        dts = _poison(dts, n_tr > 0)
+        if not lanes_given:
+            dts = {k: v[0] for k, v in dts.items()}
+        return res, dts
+
+    def jacfwd(self, *args, wrt):
+        """the Jacobian of every float output w.r.t. the broadcast operands `wrt` by forward mode: one lane per
+        operand -> {output name: array (W, *output.shape)}"""
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        _, dts = self.jvp(*args, wrt=idx, tangents=np.eye(len(idx), dtype=np.float32))
+        return dts
 
     def value_and_grad(self, *args, wrt, cotangents):
         """(Result, gradient): the forward launch and the generated replay launch"""

@@ -15,6 +15,7 @@ Launch layouts are the backend's (backend.ItemProgram): forward = [per-item][bro
 i32[3]][order] | [g f32[W]][exact words][ctl][stats] | [truncated][replay scratch].
 """
 import ctypes
+import dataclasses
 import hashlib
 import os
 
@@ -823,6 +824,29 @@ class Lowered:
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc, consts=("max_steps",), tallies=tallies,
                                ys=ys, trunc=len(ys) - 1)
         self.grads = {}
+        self.jvps = {}
+
+    def jvp_program(self, wrt, lanes):
+        """the forward-mode program: the forward's outputs and, per tangent lane, the tangents of its float tallies
+        for tangents of bc[wrt] given per launch (an input f32[lanes, len(wrt)])"""
+        from .backend import ItemProgram, TSpec, Operand
+        key = (tuple(wrt), int(lanes))
+        if key not in self.jvps:
+            for k in wrt:
+                if self.bc[k].dtype != torch.float32:
+                    raise LowerError("tallymap_b200.lower: only float32 broadcast operands have tangents")
+            if self.it.exact:
+                raise NotImplementedError("tallymap_b200: forward mode of fixed_point outputs is not lowered")
+            src, smem = jvp_source(self.it, list(wrt), int(lanes))
+            fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
+            bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
+            tallies = self.fwd.tallies + tuple(TSpec("d_" + nm, (int(lanes),) + tuple(shape)) for nm, shape in fts)
+            tallies = tuple(dataclasses.replace(t, exact=False) for t in tallies)
+            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 2 + len(self.fwd.ys)
+            kid = compile_kernel(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
+            self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc, consts=("max_steps",),
+                                         tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
+        return self.jvps[key]
 
     def grad_program(self, wrt):
         """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands)"""
@@ -845,3 +869,292 @@ class Lowered:
                                           replay_state_bytes=(stored + 3) // 4 * 4)
         return self.grads[wrt]
 
+
+
+# ------------------------------------------------------------------------------------------------ forward mode
+LANES_MAX = 16        # tangent lanes of one jvp program (the reference's jacfwd lanes, LANES_MAX_LOCAL)
+
+
+def _jvp_rule(e, a, d, out):
+    """per-lane tangent expression of equation e's output (jax's jvp rules); a: primal input expressions, d: their
+    tangent expressions (None: zero), out: the primal output expression"""
+    p = e.prim
+    x = d[0] if d else None
+    y = d[1] if len(d) > 1 else None
+
+    def plus(u, v):
+        if u is None:
+            return v
+        if v is None:
+            return u
+        return f"({u} + {v})"
+    if p == "add":
+        return plus(x, y)
+    if p == "sub":
+        return plus(x, None if y is None else f"(-{y})")
+    if p == "mul":
+        return plus(None if x is None else f"({x} * {a[1]})", None if y is None else f"({a[0]} * {y})")
+    if p == "div":
+        return plus(None if x is None else f"({x} / {a[1]})",
+                    None if y is None else f"(((-{y}) * {a[0]}) * (1.0f / ({a[1]} * {a[1]})))")
+    if p == "neg":
+        return None if x is None else f"(-{x})"
+    if p == "log":
+        return None if x is None else f"({x} / {a[0]})"
+    if p == "exp":
+        return None if x is None else f"({x} * {out})"
+    if p == "sin":
+        return None if x is None else f"({x} * tmm::cosf({a[0]}))"
+    if p == "cos":
+        return None if x is None else f"((-{x}) * tmm::sinf({a[0]}))"
+    if p == "sqrt":
+        return None if x is None else f"({x} * (0.5f / {out}))"
+    if p == "pow":
+        return plus(None if x is None else f"({x} * ({a[1]} * tmm::powf({a[0]}, {a[1]} - 1.0f)))",
+                    None if y is None else f"({y} * (tmm::logf({a[0]}) * {out}))")
+    if p == "abs":
+        return None if x is None else f"({x} * ({a[0]} > 0.0f ? 1.0f : ({a[0]} < 0.0f ? -1.0f : 0.0f)))"
+    if p in ("max", "min"):
+        return plus(None if x is None else f"({x} * ({a[0]} == {out} ? ({a[1]} == {out} ? 0.5f : 1.0f) : 0.0f))",
+                    None if y is None else f"({y} * ({a[1]} == {out} ? ({a[0]} == {out} ? 0.5f : 1.0f) : 0.0f))")
+    if p == "select":
+        db, dc = (d[1] if len(d) > 1 else None), (d[2] if len(d) > 2 else None)
+        if db is None and dc is None:
+            return None
+        return f"({a[0]} ? {db or '0.0f'} : {dc or '0.0f'})"
+    if p == "convert":
+        return x if e.outs[0].dtype == T.F32 and e.ins[0].dtype == T.F32 else None
+    if p == "floor":
+        return None
+    raise LowerError(f"tallymap_b200.lower: no jvp rule for {p}")
+
+
+def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "):
+    """straight-line primal code with each active value's L tangents; tnames: id -> [L tangent expressions]"""
+    out = []
+    for e in eqns:
+        a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        out += _emit_code([e], names, emitter, indent)
+        if e.prim == "emit":
+            v = e.ins[1]
+            if isinstance(v, T.Var) and v.id in tnames:
+                for l in range(L):
+                    out.append(indent + temitter(e.params["tally"], l, a[0], tnames[v.id][l]))
+            continue
+        if not e.outs or e.outs[0].id not in act or e.outs[0].dtype != T.F32:
+            continue
+        o = e.outs[0]
+        for l in range(L):
+            d = [tnames[x.id][l] if isinstance(x, T.Var) and x.id in tnames else None for x in e.ins]
+            expr = _jvp_rule(e, a, d, names[o.id])
+            if expr is None:
+                continue
+            out.append(f"{indent}const float d{o.id}_{l} = {expr};")
+            tnames.setdefault(o.id, [None] * L)[l] = f"d{o.id}_{l}"
+        if o.id in tnames and any(t is None for t in tnames[o.id]):
+            tnames[o.id] = [t or "0.0f" for t in tnames[o.id]]
+    return out
+
+
+def jvp_source(it, wrt, L):
+    """-> (C source of the forward ITEM with L tangent lanes of the broadcast operands bc[wrt], shared-memory bytes).
+    Buffers: [per-item][broadcast][tangent seeds f32[L, W]][consts][order] | [tallies][tangent tallies f32[L, S] of
+    the float tallies][ctl][stats] | [per-item results][truncated]"""
+    tr = it.tr
+    npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
+    if not 1 <= L <= LANES_MAX:
+        raise LowerError(f"tallymap_b200.lower: 1..{LANES_MAX} tangent lanes")
+    act, carry_act = _active(it, wrt)
+    ftal = [(t, name, shape) for t, (name, (shape, dt)) in enumerate(it.specs) if dt == T.F32]
+    lines = [PRELUDE, "namespace tmb {", "struct GenJvp {"]
+    idx = 0
+    enum = []
+    for j in range(npi):
+        enum.append(f"kIn{j} = {idx}"); idx += 1
+    for k in range(nbc):
+        enum.append(f"kBc{k} = {idx}"); idx += 1
+    enum.append(f"kTan = {idx}"); idx += 1
+    enum.append(f"kConsts = {idx}"); idx += 1
+    enum.append(f"kOrder = {idx}"); idx += 1
+    for t, _ in enumerate(it.specs):
+        enum.append(f"kT{t} = {idx}"); idx += 1
+    for q, _ in enumerate(ftal):
+        enum.append(f"kD{q} = {idx}"); idx += 1
+    enum.append(f"kCtl = {idx}"); idx += 1
+    enum.append(f"kStats = {idx}"); idx += 1
+    for r in range(len(tr.results)):
+        enum.append(f"kY{r} = {idx}"); idx += 1
+    enum.append(f"kTrunc = {idx}"); idx += 1
+    enum.append(f"kNBuf = {idx}")
+    lines.append("  enum { " + ", ".join(enum) + " };")
+    smem, priv = 0, {}
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        if S * 4 <= PRIV_BYTES:
+            priv[("p", name)] = smem
+            smem += (S * 4 + 15) // 16 * 16
+    for q, (t, name, shape) in enumerate(ftal):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        if L * S * 4 <= PRIV_BYTES:
+            priv[("d", name)] = smem
+            smem += (L * S * 4 + 15) // 16 * 16
+    lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
+    ctx = ["  struct Ctx {"]
+    for j, s in enumerate(it.in_specs[:npi]):
+        ctx.append(f"    const {_in_ctype(s)}* in{j};")
+    for k, b in enumerate(it.bc):
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+    for q, k in enumerate(wrt):
+        for l in range(L):
+            ctx.append(f"    float db{k}_{l};")
+    ctx += ["    i32 M;", "    i32* stats;", "    uint8_t* trunc;"]
+    sizes = {}
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        sizes[name] = S
+        ct = "float" if dt == T.F32 else "i32"
+        ctx.append(f"    {ct}* g{t};")
+        if ("p", name) in priv:
+            ctx.append(f"    {ct}* s{t};")
+    for q, (t, name, shape) in enumerate(ftal):
+        ctx.append(f"    float* gd{t};")
+        if ("d", name) in priv:
+            ctx.append(f"    float* sd{t};")
+    for r, y in enumerate(tr.results):
+        ctx.append(f"    {CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}* y{r};")
+    act_saved = [i for i in it.saved if i in act]
+    for i in it.saved:
+        ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
+    for i in act_saved:
+        for l in range(L):
+            ctx.append(f"    float dp{i}_{l};")
+    ctx.append("  };")
+    lines += ctx
+    lines.append("  struct State {")
+    lines.append("    i32 kc;")
+    for j, v in enumerate(tr.carry):
+        lines.append(f"    {CTYPE[v.dtype]} c{j};")
+        if carry_act[j]:
+            for l in range(L):
+                lines.append(f"    float d{j}_{l};")
+    lines.append("  };")
+    tidx = {name: t for t, (name, _) in enumerate(it.specs)}
+    lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
+    for j, s in enumerate(it.in_specs[:npi]):
+        lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
+    for k, b in enumerate(it.bc):
+        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+    for q, k in enumerate(wrt):
+        for l in range(L):
+            lines.append(f"    c.db{k}_{l} = __ldg(static_cast<const float*>(P.p[kTan]) + {l * W + q});")
+    lines += ["    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));",
+              "    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        ct = "float" if dt == T.F32 else "i32"
+        lines.append(f"    c.g{t} = static_cast<{ct}*>(P.p[kT{t}]);")
+        if ("p", name) in priv:
+            lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[('p', name)]});")
+    for q, (t, name, shape) in enumerate(ftal):
+        lines.append(f"    c.gd{t} = static_cast<float*>(P.p[kD{q}]);")
+        if ("d", name) in priv:
+            lines.append(f"    c.sd{t} = reinterpret_cast<float*>(smem + {priv[('d', name)]});")
+    for r, y in enumerate(tr.results):
+        lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
+    lines.append("  }")
+    lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
+
+    def emitter(name, idx_c, v_c):
+        t, S, dt = tidx[name], sizes[name], it.tr.specs[name][1]
+        pv = ("p", name) in priv
+        if dt == T.F32:
+            if pv:
+                return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
+            return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
+                    f"else fatom(&c.g{t}[b_], {v_c}); }}")
+        tgt = f"c.s{t}" if pv else f"c.g{t}"
+        return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
+                f"else if ({v_c}) atomicAdd(&{tgt}[b_], {v_c}); }}")
+
+    def temitter(name, l, idx_c, dv_c):
+        t, S = tidx[name], sizes[name]
+        tgt = f"c.sd{t}" if ("d", name) in priv else f"c.gd{t}"
+        # (an out-of-range index is counted once, by the primal emit)
+        return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) fatom(&{tgt}[{l * S} + b_], {dv_c}); }}"
+
+    bc_t = {it.bc[k].id: [f"c.db{k}_{l}" for l in range(L)] for k in wrt}
+    # start
+    lines.append("  __device__ static State start(Ctx& c, i64 item) {")
+    names = _names_pre(it)
+    tn = dict(bc_t)
+    for v, ld in it.loads:
+        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter)
+    for i in it.saved:
+        lines.append(f"    c.p{i} = {names[i]};")
+    for i in act_saved:
+        for l in range(L):
+            lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
+    lines += ["    State s;", "    s.kc = 0;"]
+    for j, x in enumerate(tr.carry_in):
+        lines.append(f"    s.c{j} = {_ref(x, names)};")
+        if carry_act[j]:
+            for l in range(L):
+                tv = tn[x.id][l] if isinstance(x, T.Var) and x.id in tn else "0.0f"
+                lines.append(f"    s.d{j}_{l} = {tv};")
+    lines += ["    return s;", "  }"]
+    lines += _pred_fn(it)
+    lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
+    lines.append("    return s.kc < c.M && pred(c, s);")
+    lines.append("  }")
+
+    def loop_tn(carry, state):
+        tn = dict(bc_t)
+        for i in act_saved:
+            tn[i] = [f"c.dp{i}_{l}" for l in range(L)]
+        for j, v in enumerate(carry):
+            if carry_act[j]:
+                tn[v.id] = [f"{state}.d{j}_{l}" for l in range(L)]
+        return tn
+    lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
+    names = _names_loop(it, tr.carry)
+    tn = loop_tn(tr.carry, "s")
+    lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter)
+    for j, x in enumerate(tr.body_out):
+        lines.append(f"    const {CTYPE[tr.carry[j].dtype]} n{j} = {_ref(x, names)};")
+        if carry_act[j]:
+            for l in range(L):
+                tv = tn[x.id][l] if isinstance(x, T.Var) and x.id in tn else "0.0f"
+                lines.append(f"    const float nd{j}_{l} = {tv};")
+    for j in range(len(tr.body_out)):
+        lines.append(f"    s.c{j} = n{j};")
+        if carry_act[j]:
+            for l in range(L):
+                lines.append(f"    s.d{j}_{l} = nd{j}_{l};")
+    lines += ["    s.kc += 1;", "  }"]
+    lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    names = _names_loop(it, tr.post_carry)
+    tn = loop_tn(tr.post_carry, "s")
+    lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter)
+    for r, y in enumerate(tr.results):
+        lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
+    lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
+    lines.append("  }")
+    lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
+    for t, (name, (shape, dt)) in enumerate(it.specs):
+        S = sizes[name]
+        if ("p", name) in priv:
+            if dt == T.F32:
+                lines.append(f"    SumPriv<{S}>::flush(c.s{t}, c.g{t}, tid, nth);")
+            else:
+                lines.append(f"    for (int b = tid; b < {S}; b += nth) if (c.s{t}[b]) atomicAdd(&c.g{t}[b], c.s{t}[b]);")
+    for q, (t, name, shape) in enumerate(ftal):
+        if ("d", name) in priv:
+            lines.append(f"    SumPriv<{L * sizes[name]}>::flush(c.sd{t}, c.gd{t}, tid, nth);")
+    lines.append("  }")
+    lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
+    lines.append("};")
+    lines.append("}  // namespace tmb")
+    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append("  tmb::forward_body<tmb::GenJvp>(P, n);")
+    lines.append("}")
+    return "\n".join(lines), max(smem, 16)

@@ -82,3 +82,16 @@ def test_fixed_point_sum_lowers_to_exact_bins():
     assert "ExactSum<256>::emit(c.sx0" in L.fwd_source and "ExactSum<256>::readout" in L.fwd_source
     with pytest.raises(NotImplementedError):
         tm.Sum((4,), tm.api.torch.int32, fixed_point=True)
+
+
+def test_jvp_programs_compile():
+    kx = prng.split(prng.PRNGKey(3), 8)
+    f = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), tm.api.torch.int32),
+                                "end": tm.Sum(())},
+                in_axes=(0, 0, 0, None, None), max_steps=64)
+    L = f.lowered((np.zeros((8, 3), np.float32), kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
+    p = L.jvp_program((0, 1), 2)
+    assert [t.name for t in p.tallies] == ["dep", "hits", "end", "d_dep", "d_end"]
+    assert p.tallies[3].shape == (2, 8, 8, 8) and p.tallies[4].shape == (2,)
+    with pytest.raises(lower.LowerError):
+        L.jvp_program((0,), 17)

@@ -142,3 +142,36 @@ def test_fixed_point_sums_are_order_independent(cuda, orc):
     ulps = np.abs(h.view(np.int32).astype(np.int64) - ref["hist"].view(np.int32).astype(np.int64))
     assert ulps.max() <= 1 and (ulps == 0).mean() > 0.99
     assert np.array_equal(outs[0][1], ref["side"])
+
+
+def test_jvp_walk_matches_primal_and_vjp(cuda):
+    """forward mode of the walk w.r.t. drift: the hist tangent is sum(x) per bin, i.e. the hist itself at drift = 1
+    (the same emits), and <ct, tangent> is the reverse-mode gradient"""
+    x, k = rw_inputs(50000, seed=12)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    r, d = f.jvp(x, k, np.float32(1.0), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    assert d["hist"].shape == (256,) and d["side"].shape == (2,)
+    h, dh = r.outputs["hist"].cpu().numpy(), d["hist"].cpu().numpy()
+    assert near(dh, h) and not d["side"].cpu().numpy().any()
+    ct = np.random.default_rng(3).normal(size=256).astype(np.float32)
+    g = float(f.grad(x, k, np.float32(1.0), wrt=2, cotangents={"hist": ct}))
+    assert abs(float(np.dot(ct.astype(np.float64), dh)) - g) <= 1e-4 * abs(g)
+
+
+def test_jacfwd_mixer_matches_vjp(cuda):
+    n = 4000
+    outs = {"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), torch.int32), "end": tm.Sum(())}
+    f = tm.vmap(mixer, outputs=outs, in_axes=(0, 0, 0, None, None), max_steps=64)
+    args = _mixer_args(n, 0.3, 1.7)
+    J = f.jacfwd(*args, wrt=(3, 4))
+    torch.cuda.synchronize()
+    assert J["dep"].shape == (2, 8, 8, 8) and J["end"].shape == (2,)
+    cts = {"dep": np.ones((8, 8, 8), np.float32), "end": np.float32(0.5)}
+    g = f.grad(*args, wrt=(3, 4), cotangents=cts).cpu().numpy().astype(np.float64)
+    jd = J["dep"].double().sum(dim=(1, 2, 3)).cpu().numpy() + 0.5 * J["end"].double().cpu().numpy()
+    assert np.all(np.abs(jd - g) <= 1e-4 * np.abs(g) + 1e-3), (jd, g)
+    # two lanes of arbitrary tangents: linear in the tangent
+    _, d2 = f.jvp(*args, wrt=(3, 4), tangents=[[1.0, 0.0], [2.0, -1.0]])
+    comb = 2.0 * J["dep"][0].double() - J["dep"][1].double()
+    assert torch.allclose(d2["dep"][1].double(), comb, rtol=1e-4, atol=1e-3)
