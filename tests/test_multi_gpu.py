@@ -78,3 +78,55 @@ def test_two_gpu_sharding_matches_one(cuda):
         assert np.abs(r[1].astype(np.float64) - hist1).max() <= 1e-4 * np.abs(hist1).max()
         assert np.array_equal(r[2], side1)
         assert r[4].view(np.uint32)[0] == g1[0].cpu().numpy().view(np.uint32)[0]
+
+
+def _rank_vg(rank, world, port, n, q):
+    """the fused value-and-grad launch on a shard, then the bench's collective step"""
+    import torch.distributed as dist
+    from tallymap_b200 import backend as B
+    from tallymap_b200 import parallel
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        x, k = rw_inputs(n)
+        s0, c = parallel.shard(n, rank, world)
+        out = B.run(B.RW_VG, [x[s0:s0 + c], k[s0:s0 + c]],
+                    [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)], consts=(20000,))
+        words = B.run.last["results"]["ct_drift.exact"]
+        parallel.all_reduce_sums(out[:2] + [out[3]])
+        gall = torch.zeros(1, device=dev)
+        parallel.combine_exact(words, 1, gall, out[3])
+        torch.cuda.synchronize()
+        q.put((rank, out[0].cpu().numpy(), out[4].cpu().numpy(), gall.cpu().numpy()))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_fused_value_and_grad_matches_one(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from tallymap_b200 import backend as B
+    n = 300007
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_rank_vg, args=(r, 2, port, n, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    x, k = rw_inputs(n)
+    one = B.run(B.RW_VG, [x, k], [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)],
+                consts=(20000,))
+    hist1, g1, k1 = one[0].cpu().numpy(), one[2].cpu().numpy(), one[4].cpu().numpy()
+    assert np.array_equal(np.concatenate([res[0][2], res[1][2]]), k1)
+    for r in res:
+        assert np.abs(r[1].astype(np.float64) - hist1).max() <= 1e-4 * np.abs(hist1).max()
+        assert r[3].view(np.uint32)[0] == g1.view(np.uint32)[0]
