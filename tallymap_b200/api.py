@@ -38,6 +38,30 @@ class Sum:
             raise NotImplementedError("tallymap_b200: fixed_point Sums of float32 only (the exact accumulator)")
 
 
+@dataclasses.dataclass(frozen=True)
+class Records:
+    """a Records output (tallymap.Records, _api.py:98-170): Records({field: dtype}, capacity=C).  Items append with
+    t = t.append(name, {field: value}, when=...); Result.outputs[name] is {field: tensor[C]}: record k of item i at
+    slot offset[i] + k (offset the exclusive prefix sum of the per-item counts), slots past the last record zero;
+    stats['appended'][name] the true total.  More than C records poisons the call: float fields and every float
+    Sum NaN, integer fields -1, stats['records_dropped'][name] the excess."""
+    fields: tuple
+    capacity: int
+
+    def __init__(self, fields, capacity):
+        fl = []
+        for f, dt in sorted(fields.items()):
+            if dt not in (torch.float32, torch.int32):
+                raise TypeError(f"tallymap_b200.Records: field {f!r}: float32 or int32")
+            fl.append((f, dt))
+        if not fl:
+            raise TypeError("tallymap_b200.Records needs fields")
+        if not 1 <= int(capacity) <= 2 ** 31 - 1:
+            raise ValueError("tallymap_b200.Records: capacity in [1, 2^31 - 1]")
+        object.__setattr__(self, "fields", tuple(fl))
+        object.__setattr__(self, "capacity", int(capacity))
+
+
 class Result(NamedTuple):
     outputs: dict
     per_item: Any
@@ -240,6 +264,10 @@ class MappedFn:
         self.fn = fn
         self.outputs = {}
         for name, o in outputs.items():
+            if isinstance(o, Records):
+                self.outputs[name] = ("records", o.capacity,
+                                      tuple((f, "f32" if dt == torch.float32 else "i32") for f, dt in o.fields))
+                continue
             if o.dtype not in (torch.float32, torch.int32):
                 raise TypeError(f"tallymap_b200: output {name!r}: Sum of float32 or int32")
             self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32",
@@ -300,16 +328,30 @@ class MappedFn:
         pi, bc = self._split(args)
         p = L.fwd
         out = B.run(p, pi, bc, consts=(self.max_steps,))
+        raw = B.run.last["results"]
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
         ys = out[nt + 1:]
         trunc = ys[p.trunc].bool()
-        per = [y for i, y in enumerate(ys) if i != p.trunc]
+        per = list(ys[:L.n_results])
         n_tr = trunc.sum(dtype=torch.int32)
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
-        return Result(_poison(tallies, n_tr > 0), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        bad = n_tr > 0
+        if p.records:
+            counts = {nm: ys[L.n_results + r] for r, (nm, _, _) in enumerate(p.records)}
+            recs = B.canonical_records(p, raw, counts)
+            stats["appended"] = {nm: tot for nm, (_, tot) in recs.items()}
+            stats["records_dropped"] = {nm: torch.clamp(tot - cap, min=0)
+                                        for (nm, cap, _), (_, tot) in zip(p.records, recs.values())}
+            over = any(int(v) > 0 for v in stats["records_dropped"].values())
+            bad = bad | over
+        outs = _poison(tallies, bad)
+        if p.records:
+            for nm, (rec, _) in recs.items():
+                outs[nm] = rec if not bool(n_tr > 0) else _poison(rec, n_tr > 0)
+        return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
     def grad(self, *args, wrt, cotangents, order=None):
         """d <cotangents, outputs> / d args[wrt] for float32 broadcast operand(s) `wrt`: ONE replay launch of the

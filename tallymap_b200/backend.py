@@ -76,6 +76,7 @@ class ItemProgram:
     buffers: int = 0                # nonzero: launched by its own driver with this many buffers (not by run())
     vg_fallback: str = None         # a pipelined value-and-grad program: its kernel needs C >= max_steps (two heads
                                     # per thread); with a smaller C the launch uses this fused replay kernel instead
+    records: tuple = ()             # Records outputs: ((name, capacity, ((field, torch dtype), ...)), ...)
 
     @property
     def n_args(self):
@@ -97,6 +98,14 @@ class ItemProgram:
                 # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
                 n64 = S * EXACT_WORDS + (S + 1) // 2
                 out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
+        for name, cap, fields in self.records:
+            # the raw records (a slot per append, in claim order), their keys (item, ordinal) and the slot counter
+            for f, dt in fields:
+                out.append((f"{name}.{f}", cap * 4, dt, (cap,)))
+            # (internal buffers are named with '#': a field may be called 'k')
+            out.append((f"{name}#cid", cap * 4, torch.int32, (cap,)))
+            out.append((f"{name}#k", cap * 4, torch.int32, (cap,)))
+            out.append((f"{name}#ctr", 8, torch.int64, (1,)))
         if self.queue_leaf_bytes:
             out.append(("queue.seq", max(queue, 1) * 4, torch.int32, (max(queue, 1),)))
             out.append(("queue.ctl", QCTL_WORDS * 4, torch.int32, (QCTL_WORDS,)))
@@ -122,6 +131,34 @@ class ItemProgram:
 
 def _itemsize(dt):
     return torch.empty((), dtype=dt).element_size()
+
+
+def canonical_records(p, results, counts):
+    """the reference's one-pass Records layout (tallymap/_records.py:35-62 canon): record k of item i moves from its
+    raw slot to slot offset[i] + k, offset the exclusive prefix sum of the per-item counts of the same launch; slots
+    past the last record are zero.  results: the launch's buffers by name; counts: name -> int32[N].
+    -> {name: ({field: tensor[capacity]}, total appended)}; a total beyond the capacity poisons (float fields NaN,
+    integer fields -1), as a full Queue does"""
+    out = {}
+    for name, cap, fields in p.records:
+        cnt = counts[name].to(torch.int64)
+        total = cnt.sum()
+        off = torch.cumsum(cnt, 0) - cnt
+        n = int(min(int(total), cap))
+        cid = results[f"{name}#cid"][:n].to(torch.int64)
+        pos = off[cid] + results[f"{name}#k"][:n].to(torch.int64) if n else cid
+        keep = pos < cap
+        over = int(total) > cap
+        rec = {}
+        for f, dt in fields:
+            o = torch.zeros(cap, dtype=dt, device=cnt.device)
+            if n:
+                o[pos[keep]] = results[f"{name}.{f}"][:n][keep]
+            if over:
+                o.fill_(float("nan") if dt.is_floating_point else -1)
+            rec[f] = o
+        out[name] = (rec, total)
+    return out
 
 
 _U32 = torch.int32   # uint32 key data travels as int32 bits (torch has no full uint32 arithmetic; bits only)

@@ -224,11 +224,15 @@ def _names_loop(it, carry, state="s"):
     return n
 
 
-def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False):
+def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None):
     """straight-line C for eqns; names: id -> C expression (updated with the locals defined here)"""
     out = []
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        if e.prim == "append":
+            if appender is not None:
+                out.append(indent + appender(e.params["records"], a[0], a[1:]))
+            continue
         if e.prim == "emit":
             if not skip_emits:
                 out.append(indent + emitter(e.params["tally"], a[0], a[1]))
@@ -269,10 +273,19 @@ def forward_source(it):
     for t, (name, _) in enumerate(it.specs):
         if name in it.exact:
             enum.append(f"kX{t} = {idx}"); idx += 1
+    recs = list(tr.records.items())         # [(name, (capacity, ((field, dtype), ...)))]
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f in range(len(fields)):
+            enum.append(f"kR{r}F{f} = {idx}"); idx += 1
+        enum.append(f"kR{r}Cid = {idx}"); idx += 1
+        enum.append(f"kR{r}K = {idx}"); idx += 1
+        enum.append(f"kR{r}Ctr = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
         enum.append(f"kY{r} = {idx}"); idx += 1
+    for r in range(len(recs)):
+        enum.append(f"kR{r}N = {idx}"); idx += 1
     enum.append(f"kTrunc = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
@@ -310,12 +323,20 @@ def forward_source(it):
     ctx.append("    uint8_t* trunc;")
     for i in it.saved:
         ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f, (fname, dt) in enumerate(fields):
+            ctx.append(f"    {CTYPE[dt]}* r{r}f{f};")
+        ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;", f"    i32* r{r}n;"]
+    if recs:
+        ctx.append("    i64 item;")
     ctx.append("  };")
     lines += ctx
     lines.append("  struct State {")
     lines.append("    i32 kc;")
     for j, v in enumerate(tr.carry):
         lines.append(f"    {CTYPE[v.dtype]} c{j};")
+    for r in range(len(recs)):
+        lines.append(f"    i32 a{r};   // records appended by the item so far")
     lines.append("  };")
     # setup
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -337,8 +358,29 @@ def forward_source(it):
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
     lines.append("    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);")
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f, (fname, dt) in enumerate(fields):
+            lines.append(f"    c.r{r}f{f} = static_cast<{CTYPE[dt]}*>(P.p[kR{r}F{f}]);")
+        lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);", f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
+                  f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);",
+                  f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);"]
     lines.append("  }")
     lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
+    rindex = {rname: r for r, (rname, _) in enumerate(recs)}
+
+    def appender_for(counter):
+        def appender(rname, when_c, vals_c):
+            """one record: the next raw slot of the output (one atomic, the counter keeps the true total), its
+            fields and its key (item, ordinal); -0.0 is stored as +0.0 (tallymap.Records)"""
+            r = rindex[rname]
+            cap, fields = tr.records[rname]
+            st = [f"if ({when_c}) {{ const unsigned long long o_ = atomicAdd(c.r{r}ctr, 1ull); "
+                  f"if (o_ < {int(cap)}ull) {{"]
+            for f, ((fname, dt), v) in enumerate(zip(fields, vals_c)):
+                st.append(f" c.r{r}f{f}[o_] = {v}{' + 0.0f' if dt == T.F32 else ''};")
+            st.append(f" c.r{r}cid[o_] = (i32)c.item; c.r{r}k[o_] = {counter(r)}; }} {counter(r)} += 1; }}")
+            return "".join(st)
+        return appender
 
     def emitter(name, idx_c, v_c):
         t, S, dt, pv = tinfo[name]
@@ -361,8 +403,12 @@ def forward_source(it):
     lines += _emit_code(tr.pre, names, emitter)
     for i in it.saved:
         lines.append(f"    c.p{i} = {names[i]};")
+    if recs:
+        lines.append("    c.item = item;")
     lines.append("    State s;")
     lines.append("    s.kc = 0;")
+    for r in range(len(recs)):
+        lines.append(f"    s.a{r} = 0;")
     for j, x in enumerate(tr.carry_in):
         lines.append(f"    s.c{j} = {_ref(x, names)};")
     lines.append("    return s;")
@@ -373,14 +419,18 @@ def forward_source(it):
     lines.append("  }")
     lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
     names = _names_loop(it, tr.carry)
-    lines += _emit_code(tr.body, names, emitter)
+    lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"))
     lines += _assign_carry(it, names)
     lines.append("  }")
     lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
     names = _names_loop(it, tr.post_carry)
-    lines += _emit_code(tr.post, names, emitter)
+    for r in range(len(recs)):
+        lines.append(f"    i32 a{r} = s.a{r};")
+    lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"))
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
+    for r in range(len(recs)):
+        lines.append(f"    c.r{r}n[item] = a{r};")
     lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
     lines.append("  }")
     lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
@@ -806,9 +856,11 @@ class Lowered:
     def __init__(self, fn, in_specs, n_per_item, outputs, name=None):
         from .backend import ItemProgram, TSpec
         self.name = name or getattr(fn, "__name__", "item")
+        recs = {k: (v[1], tuple(v[2])) for k, v in outputs.items() if v[0] == "records"}
+        outputs = {k: v for k, v in outputs.items() if v[0] != "records"}
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
         exact = [k for k, v in outputs.items() if len(v) > 2 and v[2]]
-        self.tr = T.trace_item(fn, in_specs, n_per_item, specs)
+        self.tr = T.trace_item(fn, in_specs, n_per_item, specs, recs)
         self.it = Item(self.tr, in_specs, self.name, exact)
         it = self.it
         src, smem = forward_source(it)
@@ -818,11 +870,15 @@ class Lowered:
         self.pi, self.bc = pi, bc
         tallies = tuple(TSpec(nm, shape, TDTYPE[dt], exact=nm in it.exact) for nm, (shape, dt) in it.specs)
         ys = tuple(_operand(f"y{r}", y.dtype) for r, y in enumerate(self.tr.results))
+        ys += tuple(_operand(f"{nm}#count", T.I32) for nm in recs)
         ys += (_operand("truncated", T.BOOL),)
-        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + 2 + len(ys)
+        records = tuple((nm, int(cap), tuple((f, TDTYPE[dt]) for f, dt in fl)) for nm, (cap, fl) in recs.items())
+        nrec = sum(len(fl) + 3 for _, _, fl in records)
+        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys)
         kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc, consts=("max_steps",), tallies=tallies,
-                               ys=ys, trunc=len(ys) - 1)
+                               ys=ys, trunc=len(ys) - 1, records=records)
+        self.n_results = len(self.tr.results)
         self.grads = {}
         self.jvps = {}
 
@@ -835,8 +891,9 @@ class Lowered:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:
                     raise LowerError("tallymap_b200.lower: only float32 broadcast operands have tangents")
-            if self.it.exact:
-                raise NotImplementedError("tallymap_b200: forward mode of fixed_point outputs is not lowered")
+            if self.it.exact or self.fwd.records:
+                raise NotImplementedError("tallymap_b200: forward mode of fixed_point or Records outputs is not "
+                                          "lowered")
             src, smem = jvp_source(self.it, list(wrt), int(lanes))
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
@@ -852,6 +909,8 @@ class Lowered:
         """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands)"""
         from .backend import ItemProgram, TSpec
         wrt = tuple(wrt)
+        if self.fwd.records:
+            raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
         if wrt not in self.grads:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:

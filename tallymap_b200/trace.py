@@ -212,10 +212,33 @@ class Key:
 
 
 class TallyToken:
-    """the tally handle `t` of an item: t.add(name, index, value) records an emit and returns the handle"""
+    """the tally handle `t` of an item: t.add(name, index, value) records an emit, t.append(name, {field: value},
+    when=...) a record; both return the handle"""
 
-    def __init__(self, specs):
+    def __init__(self, specs, records=None):
         self.specs = specs           # name -> (shape, dtype)
+        self.records = records or {}  # name -> (capacity, ((field, dtype), ...) sorted by field)
+
+    def append(self, name, fields, when=True):
+        """a Records output's append (tallymap/_tally.py:302-364): the fields of one record, written when `when`"""
+        if name not in self.records:
+            raise TraceError(f"tallymap_b200.lang: no Records output named {name!r}")
+        cap, spec = self.records[name]
+        if sorted(fields) != [f for f, _ in spec]:
+            raise TraceError(f"tallymap_b200.lang: Records {name!r} has fields {[f for f, _ in spec]}")
+        w = _lit(when)
+        if w.dtype != BOOL:
+            raise TraceError("tallymap_b200.lang: append's `when` must be bool")
+        vals = []
+        for f, dt in spec:
+            v = _lit(fields[f])
+            if isinstance(v, Lit):
+                v = Lit(float(v.value), F32) if dt == F32 else Lit(int(v.value), dt)
+            if v.dtype != dt:
+                raise TraceError(f"tallymap_b200.lang: Records {name!r} field {f!r} is {dt}, got {v.dtype}")
+            vals.append(v)
+        _cur().eqns.append(Eqn("append", [w] + vals, [], dict(records=name)))
+        return self
 
     def add(self, name, index, value):
         if name not in self.specs:
@@ -274,6 +297,7 @@ class Traced:
     post: list
     results: list            # per-item results (Var | Lit)
     specs: dict
+    records: dict = dataclasses.field(default_factory=dict)
 
 
 class _Loop:
@@ -359,9 +383,10 @@ def _flatten(tree):
     return leaves, rebuild
 
 
-def trace_item(fn, in_specs, n_per_item, specs):
+def trace_item(fn, in_specs, n_per_item, specs, records=None):
     """trace item function `fn(t, *args)`; in_specs: per argument "f32" | "i32" | "u32" | "key" | ("f32", n)
-    (a per-item vector); specs: output name -> (shape, dtype).  -> Traced"""
+    (a per-item vector); specs: Sum output name -> (shape, dtype); records: Records output name -> (capacity,
+    ((field, dtype), ...)).  -> Traced"""
     tr = Trace()
     tr.loop_state = {"depth": 0}
     args = []
@@ -372,7 +397,7 @@ def trace_item(fn, in_specs, n_per_item, specs):
             args.append(tuple(tr.new(s[0]) for _ in range(s[1])))
         else:
             args.append(tr.new(s))
-    tok = TallyToken(specs)
+    tok = TallyToken(specs, records)
     _CTX.append(tr)
     try:
         out = fn(tok, *args)
@@ -388,7 +413,9 @@ def trace_item(fn, in_specs, n_per_item, specs):
     pre = tr.eqns[:st["pre_len"]]
     post = tr.eqns[st["pre_len"]:]
     keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
+    if any(e.prim == "append" for e in pre):
+        raise TraceError("tallymap_b200.lang: append before the loop is not lowered (append in the loop or after it)")
     return Traced(inputs=args, n_per_item=n_per_item, pre=pre, carry_in=[_lit(x) for x in keep(st["init"])],
                   carry=keep(st["carry"]), cond=st["cond"], cond_out=st["cond_out"], body=st["body"],
                   body_out=[_lit(x) for x in keep(st["body_out"])], post_carry=keep(st["post_carry"]), post=post,
-                  results=results, specs=specs)
+                  results=results, specs=specs, records=records or {})

@@ -47,3 +47,17 @@ def mixer(t, pos, key, n, a, b):
     k, x, y, w, t = tl.while_loop(lambda c: c[0] < n, body, (0, x0, y0 + z0, 1.0, t))
     t = t.add("end", 0, x * a - y * b + w)
     return t, k
+
+
+def walk_records(t, x, key, drift):
+    """the walk, recording each step that starts in bin 128 (step, position) and each item's exit (steps, side)"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        b = (x * 256).astype(tl.int32)
+        t = t.add("hist", b, drift * x)
+        t = t.append("hits", {"k": k, "x": x}, when=b == 128)
+        return k + 1, x + 0.02 * (2 * u - 1), t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    t = t.append("exit", {"k": k, "side": (x > 1).astype(tl.int32)})
+    return t, k

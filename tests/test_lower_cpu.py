@@ -95,3 +95,17 @@ def test_jvp_programs_compile():
     assert p.tallies[3].shape == (2, 8, 8, 8) and p.tallies[4].shape == (2,)
     with pytest.raises(lower.LowerError):
         L.jvp_program((0,), 17)
+
+
+def test_records_lower_and_compile():
+    from items_lang import walk_records
+    outs = {"hist": tm.Sum((256,)), "hits": tm.Records({"k": tm.api.torch.int32, "x": tm.api.torch.float32},
+                                                       capacity=1024),
+            "exit": tm.Records({"k": tm.api.torch.int32, "side": tm.api.torch.int32}, capacity=16)}
+    f = tm.vmap(walk_records, outputs=outs, in_axes=(0, 0, None), max_steps=20000)
+    L = f.lowered(_args_walk())
+    names = [n for n, _, _, _ in L.fwd.result_layout(16)[0]]
+    assert names[:3] == ["hist", "hits.k", "hits.x"] and "exit#ctr" in names and "hits#count" in names
+    assert "atomicAdd(c.r0ctr, 1ull)" in L.fwd_source
+    with pytest.raises(NotImplementedError):
+        L.grad_program((0,))

@@ -175,3 +175,66 @@ def test_jacfwd_mixer_matches_vjp(cuda):
     _, d2 = f.jvp(*args, wrt=(3, 4), tangents=[[1.0, 0.0], [2.0, -1.0]])
     comb = 2.0 * J["dep"][0].double() - J["dep"][1].double()
     assert torch.allclose(d2["dep"][1].double(), comb, rtol=1e-4, atol=1e-3)
+
+
+def _walk_host(x0, keys, M=20000):
+    """the walk on the host (numpy f32, jax.random's threefry): per item its hits (step, x) in bin 128 and its exit"""
+    from tallymap_b200.prng import threefry2x32
+    x = x0.astype(np.float32).copy()
+    n = len(x)
+    alive = (x >= 0) & (x <= 1)
+    k = np.zeros(n, np.int32)
+    hits = [[] for _ in range(n)]
+    step = 0
+    with np.errstate(over="ignore"):
+        while alive.any() and step < M:
+            i = np.nonzero(alive)[0]
+            o0, o1 = threefry2x32(keys[i, 0], keys[i, 1], np.uint32(0), np.uint32(step))
+            a0, a1 = threefry2x32(o0, o1, np.uint32(0), np.uint32(0))
+            u = (((a0 ^ a1) >> np.uint32(9)) | np.uint32(0x3F800000)).view(np.float32) - np.float32(1.0)
+            b = (x[i] * np.float32(256)).astype(np.int32)
+            for j in np.nonzero(b == 128)[0]:
+                hits[i[j]].append((step, x[i[j]]))
+            x[i] = x[i] + np.float32(0.02) * (np.float32(2.0) * u - np.float32(1.0))
+            k[i] += 1
+            step += 1
+            alive = (x >= 0) & (x <= 1) & (k < M)
+    return hits, k, (x > 1).astype(np.int32)
+
+
+def test_records_canonical_layout(cuda):
+    from items_lang import walk_records
+    n = 300
+    x, k = rw_inputs(n, seed=13)
+    outs = {"hist": tm.Sum((256,)), "hits": tm.Records({"k": torch.int32, "x": torch.float32}, capacity=1 << 16),
+            "exit": tm.Records({"k": torch.int32, "side": torch.int32}, capacity=n)}
+    f = tm.vmap(walk_records, outputs=outs, in_axes=(0, 0, None), max_steps=20000)
+    r1 = f(x, k, np.float32(1.0))
+    r2 = f(x, k, np.float32(1.0))
+    torch.cuda.synchronize()
+    hits, K, side = _walk_host(x, k)
+    want_k = np.array([s for h in hits for s, _ in h], np.int32)
+    want_x = np.array([v for h in hits for _, v in h], np.float32)
+    m = len(want_k)
+    assert 0 < m < 1 << 16 and int(r1.stats["appended"]["hits"]) == m and int(r1.stats["appended"]["exit"]) == n
+    for r in (r1, r2):            # deterministic layout, whatever order the records were claimed in
+        h = {kk: v.cpu().numpy() for kk, v in r.outputs["hits"].items()}
+        assert np.array_equal(h["k"][:m], want_k) and np.array_equal(bits(h["x"][:m]), bits(want_x))
+        assert not h["k"][m:].any() and not h["x"][m:].any()
+        e = {kk: v.cpu().numpy() for kk, v in r.outputs["exit"].items()}
+        assert np.array_equal(e["k"], K) and np.array_equal(e["side"], side)
+    assert np.array_equal(r1.per_item.cpu().numpy(), K)
+
+
+def test_records_overflow_poisons(cuda):
+    from items_lang import walk_records
+    n = 300
+    x, k = rw_inputs(n, seed=13)
+    outs = {"hist": tm.Sum((256,)), "hits": tm.Records({"k": torch.int32, "x": torch.float32}, capacity=8),
+            "exit": tm.Records({"k": torch.int32, "side": torch.int32}, capacity=n)}
+    f = tm.vmap(walk_records, outputs=outs, in_axes=(0, 0, None), max_steps=20000)
+    r = f(x, k, np.float32(1.0))
+    torch.cuda.synchronize()
+    assert int(r.stats["records_dropped"]["hits"]) == int(r.stats["appended"]["hits"]) - 8 > 0
+    assert (r.outputs["hits"]["k"].cpu().numpy() == -1).all() and torch.isnan(r.outputs["hits"]["x"]).all()
+    assert torch.isnan(r.outputs["hist"]).all()
