@@ -21,7 +21,7 @@ from . import _lib
 STATS = ("spawned", "children_dropped", "children_truncated", "fixed_point_overflow", "dropped_emits")
 CTL_WORDS = 8
 EXACT_WORDS = 5
-QCTL_WORDS = 5 * 32         # the spawn ring's control words, one 128-byte line each
+QCTL_WORDS = 6 * 32         # the spawn ring's control words, one 128-byte line each
 QUEUE_DEFAULT = 1 << 22     # ring slots of a spawning program (64 MiB of leaves for the shower)
 
 

@@ -23,7 +23,7 @@
 //
 // Buffers:
 //   sh_fwd   E0 f32[N], depth0 f32[N], keys u32[N,2], X0 f32, consts i32[2] (max_steps, Q), order |
-//            dep f32[512], count i32[1], seq u32[Q], qctl u32[5*32], ctl, stats | k i32[N], trunc u8[N],
+//            dep f32[512], count i32[1], seq u32[Q], qctl u32[6*32], ctl, stats | k i32[N], trunc u8[N],
 //            ring (E, depth, key)[Q]
 #pragma once
 #include "tm_math.h"
@@ -86,6 +86,7 @@ struct SHFwd {
     i32* stats;
     i32* kout;
     uint8_t* trunc;
+    mutable i32 n;     // particles this thread finished
   };
   __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
     c.E0 = static_cast<const float*>(P.p[kE0]);
@@ -100,6 +101,7 @@ struct SHFwd {
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.kout = static_cast<i32*>(P.p[kK]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.n = 0;
   }
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static State start(Ctx& c, i64 item) {
@@ -110,18 +112,18 @@ struct SHFwd {
     return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
-  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child* out, int* n_out) {
+  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
     const ShowerStepOut o = shower_advance(c.X0, s);
     if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
     if (o.split) {
       const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
-      out[0] = Child{s.E * o.z, s.depth, c0.a, c0.b};
-      out[1] = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
-      *n_out = 2;
+      o0 = Child{s.E * o.z, s.depth, c0.a, c0.b};
+      o1 = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
+      n_out = 2;
     }
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {
-    atomicAdd(c.shc, 1);                                   // count: Sum((1,)) int32, privatised
+    c.n += 1;                                              // count: Sum((1,)) int32, per thread, then per block
     const bool tr = s.kc >= c.M && s.alive;
     if (child) {
       if (tr) atomicAdd(&c.stats[kStChildrenTruncated], 1);
@@ -132,6 +134,8 @@ struct SHFwd {
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
     SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.dep, tid, nth);
+    if (c.n) atomicAdd(c.shc, c.n);
+    __syncthreads();
     if (tid == 0) {
       const i32 v = *reinterpret_cast<const i32*>(smem + kNB * 4);
       if (v) atomicAdd(c.count, v);
@@ -178,7 +182,7 @@ struct ShowerRecState {
 
 // the recording forward (rec_primal, _reverse_spawn.py:85-109): the forward's outputs, plus the record.
 //   sh_rec   E0 f32[N], depth0 f32[N], keys u32[N,2], X0 f32, consts i32[3] (max_steps, Q, R), order |
-//            dep f32[512], count i32[1], seq u32[Q], qctl u32[5*32], ctl, stats, tree u64[4] (0: children
+//            dep f32[512], count i32[1], seq u32[Q], qctl u32[6*32], ctl, stats, tree u64[4] (0: children
 //            recorded or not) | k i32[N], trunc u8[N], last i32[N], ring ShowerRecChild[Q], record ShowerRecord[R]
 struct SHRec {
   enum { kE0, kDepth0, kKeys, kX0, kConsts, kOrder, kDep, kCount, kSeq, kQctl, kCtl, kStats, kTree, kK, kTrunc,
@@ -204,6 +208,7 @@ struct SHRec {
     uint8_t* trunc;
     i32* lastout;
     ShowerRecord* rec;
+    mutable i32 n;     // particles this thread finished
   };
   __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
     const i32* consts = static_cast<const i32*>(P.p[kConsts]);
@@ -223,6 +228,7 @@ struct SHRec {
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
     c.lastout = static_cast<i32*>(P.p[kLast]);
     c.rec = static_cast<ShowerRecord*>(P.p[kRecord]);
+    c.n = 0;
   }
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static State start(Ctx& c, i64 item) {
@@ -233,7 +239,7 @@ struct SHRec {
     return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true, ch.slot, ch.gen, -1};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
-  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child* out, int* n_out) {
+  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
     const ShowerStepOut o = shower_advance(c.X0, s);
     if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
     // record slots for the children of this iteration's splitting lanes: one atomic per warp
@@ -252,13 +258,13 @@ struct SHRec {
       if (r0 >= 0) c.rec[r0] = ShowerRecord{e0, s.depth, c0.a, c0.b, s.last, -1, s.gen + 1, 0};
       if (r1 >= 0) c.rec[r1] = ShowerRecord{e1, s.depth, c1.a, c1.b, r0, -1, s.gen + 1, 0};
       s.last = r1;
-      out[0] = Child{e0, s.depth, c0.a, c0.b, r0, s.gen + 1};
-      out[1] = Child{e1, s.depth, c1.a, c1.b, r1, s.gen + 1};
-      *n_out = 2;
+      o0 = Child{e0, s.depth, c0.a, c0.b, r0, s.gen + 1};
+      o1 = Child{e1, s.depth, c1.a, c1.b, r1, s.gen + 1};
+      n_out = 2;
     }
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {
-    atomicAdd(c.shc, 1);
+    c.n += 1;
     const bool tr = s.kc >= c.M && s.alive;
     if (child) {
       if (tr) atomicAdd(&c.stats[kStChildrenTruncated], 1);
@@ -271,6 +277,8 @@ struct SHRec {
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
     SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.dep, tid, nth);
+    if (c.n) atomicAdd(c.shc, c.n);
+    __syncthreads();
     if (tid == 0) {
       const i32 v = *reinterpret_cast<const i32*>(smem + kNB * 4);
       if (v) atomicAdd(c.count, v);

@@ -11,10 +11,11 @@
 // 2L + 2 by its consumer.  Control words sit on separate 128-byte lines (the reference's QCTL_STRIDE, kernel.py:307).
 //
 // Work sharing: a lane keeps the children it spawns on a private stack (kPrivate entries in local memory) and runs
-// them depth-first, with no atomics, while the shared ring holds at least kShareLow pending children; below that
-// (lanes are running dry) its children go to the ring for any lane to pop.  A breadth-first FIFO over 10^6 roots
+// them depth-first, with no atomics, unless lanes are hungry: a lane that finds no work counts itself in the hungry
+// word until it gets some, and a lane that spawns shares its children through the ring while the ring holds fewer
+// pending children than there are hungry lanes.  So the ring carries only the children other lanes are waiting for.  A breadth-first FIFO over 10^6 roots
 // would need a ring as wide as the whole forest's frontier (the reference sizes its Queue to the pending children);
-// depth-first lanes keep the ring near kShareLow, so it never overflows and a count is deterministic.  Children run
+// depth-first lanes share only what hungry lanes wait for, so the ring never overflows and a count is deterministic.
 // in a different order than the reference's ring runs them, which changes no tally bit beyond float summation order.
 //
 // Termination: a lane is counted in flight from its claim (root) or global pop (child) until it has finished its item
@@ -32,24 +33,34 @@
 namespace tmb {
 
 constexpr int kQStride = 32;      // u32 words between control words (128 B)
-enum { kQTail = 0, kQHead = 1, kQPending = 2, kQOcc = 3, kQFlight = 4, kQWords = 5 };
+enum { kQTail = 0, kQHead = 1, kQPending = 2, kQOcc = 3, kQFlight = 4, kQHungry = 5, kQWords = 6 };
 constexpr u32 kSpinLimit = 1u << 22;   // polls of a slot sequence word (~0.3 s with the back-off)
 constexpr u64 kIdleLimitNs = 20000000000ull;   // 20 s without progress: give up (the error word says so)
 constexpr int kPrivate = 48;       // a lane's private stack of children (a shower's tree is < 80 generations deep)
-constexpr i32 kShareLow = 8192;    // share children through the ring while it holds fewer than this many
 
 __device__ __forceinline__ u32* qword(u32* q, int w) { return q + w * kQStride; }
 __device__ __forceinline__ u32 ld_volatile(const u32* p) { return *reinterpret_cast<const volatile u32*>(p); }
+// a slot's sequence word: published / freed with release stores, polled with acquire loads, so the leaves written
+// before a release are visible to the reader after its acquire (no full fences on the ring's data path)
+__device__ __forceinline__ u32 ld_acquire(const u32* p) {
+  u32 v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(u32* p, u32 v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ u64 globaltimer() {
   u64 t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 
-// wait (bounded) until seq[slot] == want; false if the wait gave up
+// wait (bounded) until seq[slot] == want (an acquire: what was written before its publication is visible); false if
+// the wait gave up
 __device__ __forceinline__ bool wait_seq(const u32* seq, u32 slot, u32 want) {
   for (u32 i = 0; i < kSpinLimit; ++i) {
-    if (ld_volatile(&seq[slot]) == want) return true;
+    if (ld_acquire(&seq[slot]) == want) return true;
     __nanosleep(64);
   }
   return false;
@@ -60,7 +71,7 @@ __device__ __forceinline__ bool wait_seq(const u32* seq, u32 slot, u32 want) {
 //   kQueue, kSeq, kQctl        buffer indices of the ring (Child[Q]), its sequence words (u32[Q]) and control words
 //   kConstQ                    index of Q in the launch constants
 //   start_child(Ctx&, const Child&) -> State       a popped child's pre-loop code
-//   step(const Ctx&, State&, Child* out, int* n_out)   one step; up to 2 children to spawn
+//   step(const Ctx&, State&, Child& o0, Child& o1, int& n_out)   one step; up to 2 children to spawn
 //   finish(const Ctx&, const State&, i64 item, bool child)   post-loop code; per-item results for roots only
 template <class I>
 __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i64 n_items) {
@@ -85,8 +96,9 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
 
   typename I::State x;
   i64 item = 0;
-  bool active = false, alive = true, child = false, roots_left = true;
+  bool active = false, alive = true, child = false, roots_left = true, hungry = false;
   u64 idle_since = 0;
+  u32 spawned = 0;                  // this thread's spawned children, added to stats[0] once at the end
   Child stk[kPrivate];
   int ns = 0;
   for (;;) {
@@ -122,10 +134,8 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
       if (needy && rank < avail) {
         const u32 t = head + rank, slot = t % Q, lap = t / Q;
         if (wait_seq(seq, slot, 2u * lap + 1u)) {
-          __threadfence();
           const Child ch = ring[slot];
-          __threadfence();
-          atomicExch(&seq[slot], 2u * lap + 2u);
+          st_release(&seq[slot], 2u * lap + 2u);      // (the read above completes before the slot is free)
           atomicSub(qword(q, kQOcc), 1u);
           x = I::start_child(cx, ch);
           child = true;
@@ -163,18 +173,30 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
       if (got) {
         active = true;
         idle_since = 0;
+        if (hungry) {
+          atomicSub(qword(q, kQHungry), 1u);
+          hungry = false;
+        }
       } else if (needy) {
-        // nothing to run: leave once nothing is in flight or pending (bounded by the idle limit)
+        // nothing to run: count as hungry; leave once nothing is in flight or pending (bounded by the idle limit)
+        if (!hungry) {
+          atomicAdd(qword(q, kQHungry), 1u);
+          hungry = true;
+        }
         const u32 fl = ld_volatile(qword(q, kQFlight));
         const i32 pe = (i32)ld_volatile(qword(q, kQPending));
         if (!roots_left && fl == 0u && pe <= 0) {
           alive = false;
+          atomicSub(qword(q, kQHungry), 1u);
+          hungry = false;
         } else {
           const u64 now = globaltimer();
           if (idle_since == 0) idle_since = now;
           if (now - idle_since > kIdleLimitNs) {
             atomicOr(&ctl[kCtlError], 1u);
             alive = false;
+            atomicSub(qword(q, kQHungry), 1u);
+            hungry = false;
           }
           __nanosleep(256);
         }
@@ -183,27 +205,34 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
     if (!__any_sync(0xffffffffu, alive)) break;
 
     // ---- one step for every lane that has an item
-    Child out[2];
+    Child o0, o1;
     int n_out = 0;
     bool done = false;
     if (active) {
       if (I::cond(cx, x)) {
-        I::step(cx, x, out, &n_out);
+        I::step(cx, x, o0, o1, n_out);
       } else {
         done = true;
       }
     }
-    // ---- spawned children: onto the private stack while the ring is well stocked, else (or when the stack is
-    // full) into the ring, warp-aggregated
+    // ---- spawned children: onto the private stack unless lanes are hungry for them (or the stack is full), else
+    // into the ring, warp-aggregated
     if (n_out > 0) {
-      atomicAdd(&stats[kStSpawned], n_out);
-      const bool share = (i32)ld_volatile(qword(q, kQPending)) < kShareLow;
+      spawned += (u32)n_out;
+      const bool share =
+          (i32)ld_volatile(qword(q, kQPending)) < (i32)ld_volatile(qword(q, kQHungry));
       int ng = 0;
-      for (int j = 0; j < n_out; ++j) {
-        if (!share && ns < kPrivate) stk[ns++] = out[j];
-        else out[ng++] = out[j];
+      if (!share && ns < kPrivate) stk[ns++] = o0;
+      else ng = 1;
+      if (n_out > 1) {
+        if (!share && ns < kPrivate) {
+          stk[ns++] = o1;
+        } else {
+          if (ng == 0) o0 = o1;
+          ++ng;
+        }
       }
-      n_out = ng;
+      n_out = ng;                    // the children left for the ring: o0 (and o1)
     }
     const unsigned mp = __ballot_sync(0xffffffffu, n_out > 0);
     if (mp) {
@@ -233,9 +262,8 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
         if (off + j >= allowed) break;
         const u32 t = base + off + j, slot = t % Q, lap = t / Q;
         if (wait_seq(seq, slot, 2u * lap)) {
-          ring[slot] = out[j];
-          __threadfence();
-          atomicExch(&seq[slot], 2u * lap + 1u);
+          ring[slot] = j == 0 ? o0 : o1;
+          st_release(&seq[slot], 2u * lap + 1u);      // (the leaves above are visible to whoever acquires this)
           ++published;
         } else {
           // the slot never freed: publish nothing there (its ticket is lost: a consumer waiting on it times out)
@@ -258,6 +286,7 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
       }
     }
   }
+  if (spawned) atomicAdd(&stats[kStSpawned], (i32)spawned);
   __syncthreads();
   I::flush(cx, smem, threadIdx.x, blockDim.x);
   finish_block<I>(cx, ctl);
