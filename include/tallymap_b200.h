@@ -108,14 +108,17 @@ int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bin
 
 /* Generation lists of a recorded spawn tree, the launch order of the tree adjoint (replaces the XLA ordering of
  * tallymap/_reverse_spawn.py:255-283 inside tree_vjp; the adjoint launches themselves go through tm_launch with the
- * generation's list as the claim order).  `records`: n_records records of record_bytes bytes, each with an int32
- * generation at byte gen_offset.  On `stream`: counts[g] (uint64[n_gen + 1]) = the records of generation g, with
- * generations outside [0, n_gen) counted in counts[n_gen] and listed nowhere; lists (int32[n_records]) = the record
- * indices grouped by generation, generation g at [sum(counts[:g]), sum(counts[:g + 1])), in no particular order within
- * a generation; cursor (uint64[n_gen + 1]) is scratch.  n_gen <= TM_TREE_MAX_GEN, n_records < 2^31. */
+ * generation's list as the claim order).  `records`: n_records records of record_bytes bytes, each with its
+ * generation at byte gen_offset, an integer of gen_bytes bytes (2: uint16, 4: int32) -- a record array, or a compact
+ * array of generations (record_bytes = gen_bytes, gen_offset = 0).  On `stream`: counts[g] (uint64[n_gen + 1]) = the
+ * records of generation g, with generations outside [0, n_gen) counted in counts[n_gen] and listed nowhere; lists
+ * (int32[n_records]) = the record indices grouped by generation, generation g at [sum(counts[:g]),
+ * sum(counts[:g + 1])), in no particular order within a generation; cursor (uint64[n_gen + 1]) is scratch.
+ * n_gen <= TM_TREE_MAX_GEN, n_records < 2^31. */
 #define TM_TREE_MAX_GEN 8192
 int tm_tree_generations(void* stream, const void* records, int64_t n_records, int32_t record_bytes,
-                        int32_t gen_offset, int32_t n_gen, uint64_t* counts, uint64_t* cursor, int32_t* lists);
+                        int32_t gen_offset, int32_t gen_bytes, int32_t n_gen, uint64_t* counts, uint64_t* cursor,
+                        int32_t* lists);
 
 /* Calibration probe for rooflines: `iters` threefry2x32 evaluations per thread on every resident thread slot of
  * the device (at most out_len threads, a multiple of 128), no memory traffic besides one word per thread.

@@ -93,7 +93,7 @@ def lib():
         L.tm_exact_scatter_noalloc.argtypes = [P, P, P, i64, i32, P, P]
         L.tm_math_eval.argtypes = [P, i32, P, P, P, i64]
         L.tm_probe_threefry.argtypes = [P, i32, P, i64, ctypes.POINTER(i64)]
-        L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, P, P, P]
+        L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, i32, P, P, P]
         L.tm_compile_register.argtypes = [i64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]
         _HANDLE = L
         return L

@@ -126,6 +126,7 @@ class ItemProgram:
         if self.record_bytes:
             n = max(record, 1) * self.record_bytes // 4
             out.append(("record", n * 4, torch.int32, (n,)))
+            out.append(("record.gen", max(record, 1) * 2, torch.int16, (max(record, 1),)))
         return out, n_zero
 
 
@@ -410,12 +411,12 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
 # The record of a spawning program's reverse mode holds every child ever spawned (a slot is never reused, the
 # reference's condition for a complete record: tallymap/_reverse_spawn.py:30-33).  Its capacity R is the user's
 # `record`, else RECORD_PER_ROOT slots per root (at least RECORD_MIN), at most what RECORD_BUDGET_FRACTION of the free
-# device memory holds at RECORD_SLOT_BYTES per slot (the record, the generation lists and the children's
-# cotangents), below 2^31.  A tree with more children than R is not recorded in full: its gradient is NaN.
+# device memory holds at RECORD_SLOT_BYTES per slot (the record, its compact generation, the generation lists and the
+# children's cotangents), below 2^31.  A tree with more children than R is not recorded in full: its gradient is NaN.
 RECORD_PER_ROOT = 16384
 RECORD_MIN = 1 << 20
 RECORD_BUDGET_FRACTION = 0.5
-RECORD_SLOT_BYTES = 32 + 4 + 8
+RECORD_SLOT_BYTES = 32 + 2 + 4 + 8
 _RECORD = {}
 
 
@@ -479,8 +480,9 @@ def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_che
     counts = torch.empty(TREE_MAX_GEN + 1, dtype=torch.int64, device=dev)
     cursor = torch.empty_like(counts)
     lists = torch.empty(max(n_rec, 1), dtype=torch.int32, device=dev)
-    _lib.check(L.tm_tree_generations(ctypes.c_void_p(st), ctypes.c_void_p(rec.data_ptr()), n_rec,
-                                     SH_REC.record_bytes, 24, TREE_MAX_GEN, ctypes.c_void_p(counts.data_ptr()),
+    gens = res["record.gen"]                # (the records' generations, u16: 2 bytes a record to read)
+    _lib.check(L.tm_tree_generations(ctypes.c_void_p(st), ctypes.c_void_p(gens.data_ptr()), n_rec, 2, 0, 2,
+                                     TREE_MAX_GEN, ctypes.c_void_p(counts.data_ptr()),
                                      ctypes.c_void_p(cursor.data_ptr()), ctypes.c_void_p(lists.data_ptr())))
     cnt = counts.cpu().numpy()                                              # (second sync)
     offs = np.concatenate([[0], np.cumsum(cnt)])

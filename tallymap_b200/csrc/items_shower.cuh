@@ -183,10 +183,11 @@ struct ShowerRecState {
 // the recording forward (rec_primal, _reverse_spawn.py:85-109): the forward's outputs, plus the record.
 //   sh_rec   E0 f32[N], depth0 f32[N], keys u32[N,2], X0 f32, consts i32[3] (max_steps, Q, R), order |
 //            dep f32[512], count i32[1], seq u32[Q], qctl u32[6*32], ctl, stats, tree u64[4] (0: children
-//            recorded or not) | k i32[N], trunc u8[N], last i32[N], ring ShowerRecChild[Q], record ShowerRecord[R]
+//            recorded or not) | k i32[N], trunc u8[N], last i32[N], ring ShowerRecChild[Q], record ShowerRecord[R],
+//            gen u16[R] (each record's generation, compact)
 struct SHRec {
   enum { kE0, kDepth0, kKeys, kX0, kConsts, kOrder, kDep, kCount, kSeq, kQctl, kCtl, kStats, kTree, kK, kTrunc,
-         kLast, kQueue, kRecord, kNBuf };
+         kLast, kQueue, kRecord, kGen, kNBuf };
   enum { kConstM, kConstQ, kConstR };
   static constexpr int kNB = 512;
   static constexpr int kSmemBytes = kNB * 4 + 16;
@@ -208,6 +209,7 @@ struct SHRec {
     uint8_t* trunc;
     i32* lastout;
     ShowerRecord* rec;
+    unsigned short* gen;   // each child's generation again, compact (the generation lists read these)
     mutable i32 n;     // particles this thread finished
   };
   __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
@@ -228,6 +230,7 @@ struct SHRec {
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
     c.lastout = static_cast<i32*>(P.p[kLast]);
     c.rec = static_cast<ShowerRecord*>(P.p[kRecord]);
+    c.gen = static_cast<unsigned short*>(P.p[kGen]);
     c.n = 0;
   }
   __device__ static void stage(const Params&, unsigned char*) {}
@@ -255,8 +258,15 @@ struct SHRec {
       const float e0 = s.E * o.z, e1 = s.E * (1.0f - o.z);
       const i32 r0 = (u64)base < c.R ? (i32)base : -1;
       const i32 r1 = (u64)base + 1 < c.R ? (i32)(base + 1) : -1;
-      if (r0 >= 0) c.rec[r0] = ShowerRecord{e0, s.depth, c0.a, c0.b, s.last, -1, s.gen + 1, 0};
-      if (r1 >= 0) c.rec[r1] = ShowerRecord{e1, s.depth, c1.a, c1.b, r0, -1, s.gen + 1, 0};
+      const unsigned short g16 = (unsigned short)(s.gen + 1 < 65535 ? s.gen + 1 : 65535);
+      if (r0 >= 0) {
+        c.rec[r0] = ShowerRecord{e0, s.depth, c0.a, c0.b, s.last, -1, s.gen + 1, 0};
+        c.gen[r0] = g16;
+      }
+      if (r1 >= 0) {
+        c.rec[r1] = ShowerRecord{e1, s.depth, c1.a, c1.b, r0, -1, s.gen + 1, 0};
+        c.gen[r1] = g16;
+      }
       s.last = r1;
       o0 = Child{e0, s.depth, c0.a, c0.b, r0, s.gen + 1};
       o1 = Child{e1, s.depth, c1.a, c1.b, r1, s.gen + 1};

@@ -81,24 +81,37 @@ __global__ void exact_readout_kernel(const u64* words, int n_bins, float* out, i
 // the backend's f32 math on the device, elementwise (fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y))
 // ---- generation lists of a recorded spawn tree.  The reference orders each generation of the record with XLA
 // scatters and a while loop (tallymap/_reverse_spawn.py:255-283) and launches the adjoint one generation at a time.
-// Records are `stride` bytes apart with an int32 generation at byte `gen_off`; generations >= n_gen (or < 0) are
-// counted in counts[n_gen] and listed nowhere (the host poisons the gradient: the reference's
-// 'generation_overflow').  Within a generation the list order is arbitrary (a warp-aggregated cursor per
-// generation): each adjoint item writes only its own slot, and broadcast cotangents are exact tallies.
+// Record r's generation is an integer of gen_bytes bytes (2: u16, 4: i32) at byte gen_off + r * stride; generations
+// >= n_gen (or < 0) are counted in counts[n_gen] and listed nowhere (the host poisons the gradient: the reference's
+// 'generation_overflow').  Within a generation the list order is arbitrary: each adjoint item writes only its own
+// slot, and broadcast cotangents are exact tallies.
 __device__ __forceinline__ int tree_gen_of(const unsigned char* rec, long long r, int stride, int gen_off,
-                                           int n_gen) {
-  const int g = *reinterpret_cast<const int*>(rec + r * stride + gen_off);
+                                           int gen_bytes, int n_gen) {
+  const unsigned char* p = rec + r * stride + gen_off;
+  const int g = gen_bytes == 2 ? (int)*reinterpret_cast<const unsigned short*>(p) : *reinterpret_cast<const int*>(p);
   return (g >= 0 && g < n_gen) ? g : n_gen;
 }
 
+// add 1 for this lane to counter[g] in shared memory, lanes of a warp with the same g sharing one atomic; -> the
+// counter's value before this lane's add
+__device__ __forceinline__ u32 shared_add_one(u32* counter, int g) {
+  const int lane = threadIdx.x & 31;
+  const unsigned peers = __match_any_sync(__activemask(), g);
+  const int leader = __ffs(peers) - 1;
+  u32 base = 0u;
+  if (lane == leader) base = atomicAdd(&counter[g], (u32)__popc(peers));
+  base = __shfl_sync(peers, base, leader);
+  return base + __popc(peers & ((1u << lane) - 1u));
+}
+
 // counts[g] += the records of generation g (shared-memory histogram of n_gen + 1 bins per block)
-__global__ void tree_hist_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int n_gen,
-                                 unsigned long long* counts) {
+__global__ void tree_hist_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int gen_bytes,
+                                 int n_gen, unsigned long long* counts) {
   extern __shared__ u32 hist[];
   for (int i = threadIdx.x; i <= n_gen; i += blockDim.x) hist[i] = 0u;
   __syncthreads();
   for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x)
-    atomicAdd(&hist[tree_gen_of(rec, r, stride, gen_off, n_gen)], 1u);
+    shared_add_one(hist, tree_gen_of(rec, r, stride, gen_off, gen_bytes, n_gen));
   __syncthreads();
   for (int i = threadIdx.x; i <= n_gen; i += blockDim.x)
     if (hist[i]) atomicAdd(&counts[i], (unsigned long long)hist[i]);
@@ -114,19 +127,30 @@ __global__ void tree_scan_kernel(const unsigned long long* counts, int n_gen, un
   }
 }
 
-// lists[cursor[g]++] = r for every record r of generation g < n_gen (lanes of a warp with the same generation share
-// one atomic)
-__global__ void tree_scatter_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int n_gen,
-                                   unsigned long long* cursor, i32* lists) {
-  const int lane = threadIdx.x & 31;
-  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x) {
-    const int g = tree_gen_of(rec, r, stride, gen_off, n_gen);
-    const unsigned peers = __match_any_sync(__activemask(), g);
-    const int leader = __ffs(peers) - 1;
-    unsigned long long base = 0ull;
-    if (lane == leader) base = atomicAdd(&cursor[g], (unsigned long long)__popc(peers));
-    base = __shfl_sync(peers, base, leader);
-    if (g < n_gen) lists[base + __popc(peers & ((1u << lane) - 1u))] = (i32)r;
+// lists[...] = r for every record r of generation g < n_gen, grouped by generation.  A block takes a contiguous chunk
+// of the records: it counts the chunk's generations in shared memory, reserves its range of each generation's list
+// with one global atomic per generation, then places its records with shared-memory counters (one global atomic per
+// generation per block instead of one per warp and generation)
+__global__ void tree_scatter_kernel(const unsigned char* rec, long long n, int stride, int gen_off, int gen_bytes,
+                                    int n_gen, unsigned long long* cursor, i32* lists) {
+  extern __shared__ u32 sh[];
+  u32* const cnt = sh;                       // [n_gen + 1]
+  unsigned long long* const base = reinterpret_cast<unsigned long long*>(sh + ((n_gen + 2) & ~1));
+  const long long chunk = (n + gridDim.x - 1) / gridDim.x;
+  const long long lo = (long long)blockIdx.x * chunk, hi = lo + chunk < n ? lo + chunk : n;
+  for (int i = threadIdx.x; i <= n_gen; i += blockDim.x) cnt[i] = 0u;
+  __syncthreads();
+  for (long long r = lo + threadIdx.x; r < hi; r += blockDim.x)
+    shared_add_one(cnt, tree_gen_of(rec, r, stride, gen_off, gen_bytes, n_gen));
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_gen; i += blockDim.x) {
+    base[i] = cnt[i] ? atomicAdd(&cursor[i], (unsigned long long)cnt[i]) : 0ull;
+    cnt[i] = 0u;
+  }
+  __syncthreads();
+  for (long long r = lo + threadIdx.x; r < hi; r += blockDim.x) {
+    const int g = tree_gen_of(rec, r, stride, gen_off, gen_bytes, n_gen);
+    if (g < n_gen) lists[base[g] + shared_add_one(cnt, g)] = (i32)r;
   }
 }
 

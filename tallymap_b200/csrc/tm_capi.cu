@@ -466,10 +466,11 @@ int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bin
 }
 
 int tm_tree_generations(void* stream, const void* records, int64_t n_records, int32_t record_bytes,
-                        int32_t gen_offset, int32_t n_gen, uint64_t* counts, uint64_t* cursor, int32_t* lists) {
-  if (n_records < 0 || n_records > INT32_MAX || record_bytes < 4 || record_bytes % 4 || gen_offset < 0 ||
-      gen_offset % 4 || gen_offset + 4 > record_bytes || n_gen < 1 || n_gen > TM_TREE_MAX_GEN || !counts ||
-      !cursor || (n_records > 0 && (!records || !lists)))
+                        int32_t gen_offset, int32_t gen_bytes, int32_t n_gen, uint64_t* counts, uint64_t* cursor,
+                        int32_t* lists) {
+  if (n_records < 0 || n_records > INT32_MAX || (gen_bytes != 2 && gen_bytes != 4) || record_bytes < gen_bytes ||
+      record_bytes % gen_bytes || gen_offset < 0 || gen_offset % gen_bytes || gen_offset + gen_bytes > record_bytes ||
+      n_gen < 1 || n_gen > TM_TREE_MAX_GEN || !counts || !cursor || (n_records > 0 && (!records || !lists)))
     return fail(TM_EINVAL, "tallymap_b200: tm_tree_generations: bad arguments");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)(n_gen + 1) * 8, st);
@@ -484,13 +485,18 @@ int tm_tree_generations(void* stream, const void* records, int64_t n_records, in
   unsigned long long* const cnt = reinterpret_cast<unsigned long long*>(counts);
   unsigned long long* const cur = reinterpret_cast<unsigned long long*>(cursor);
   tmb::tree_hist_kernel<<<(unsigned)grid, 256, (size_t)(n_gen + 1) * 4, st>>>(rec, n_records, record_bytes,
-                                                                               gen_offset, n_gen, cnt);
+                                                                               gen_offset, gen_bytes, n_gen, cnt);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_hist_kernel", e);
   tmb::tree_scan_kernel<<<1, 32, 0, st>>>(cnt, n_gen, cur);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_scan_kernel", e);
   if (n_records > 0) {
-    tmb::tree_scatter_kernel<<<(unsigned)grid, 256, 0, st>>>(rec, n_records, record_bytes, gen_offset, n_gen, cur,
-                                                             lists);
+    const size_t smem = (size_t)((n_gen + 2) & ~1) * 4 + (size_t)n_gen * 8;
+    if (smem > 48 * 1024) {
+      e = cudaFuncSetAttribute(tmb::tree_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+    }
+    tmb::tree_scatter_kernel<<<(unsigned)grid, 256, smem, st>>>(rec, n_records, record_bytes, gen_offset, gen_bytes,
+                                                               n_gen, cur, lists);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("tree_scatter_kernel", e);
   }
   return TM_OK;
