@@ -331,6 +331,8 @@ def main():
     # the fused value-and-grad launch (what value_and_grad runs for cotangents given up front), when the item has one
     fused = None if (tree or args.unfused) else tm.FAMILIES[FAM[cfg.name]].fused.get((0,) if len(cfg.bc) == 1
                                                                                        else tuple(range(len(cfg.bc))))
+    if fused is not None and not B.pipelined(fused, cfg.max_steps, dev):
+        fused = None                  # (as value_and_grad: the fused replay would be slower than two launches)
     vo = None if fused is None else B.alloc_results(fused, N, dev, max_steps=cfg.max_steps)
     vnames = None if fused is None else [n for n, _, _, _ in fused.result_layout(N)[0]]
 

@@ -213,7 +213,7 @@ class Mapped:
             if all(b in key for b in bpos):
                 prog, sel = g, [key.index(b) for b in bpos]
                 break
-        if prog is None:
+        if prog is None or not B.pipelined(prog, self.max_steps):
             return None
         pi, bc = self._split(args)
         n = int(pi[0].shape[0]) if pi else 0

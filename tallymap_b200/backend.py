@@ -308,6 +308,16 @@ def replay_scratch_states(C, max_steps, pipelined=False):
     return 3 * C + 1
 
 
+def pipelined(p, max_steps, device=None):
+    """whether fused value-and-grad program p runs its pipelined kernel at max_steps on this device (its ring tape of
+    every resident thread fits), rather than the fused checkpointed replay, which is slower than a forward launch and
+    a replay launch (a warp pays for its counting and its sweeping lanes at once)"""
+    if p.vg_fallback is None:
+        return False
+    C = replay_plan(p, max_steps, None, device)[0]
+    return C + 1 == ring_states(max_steps)
+
+
 def ring_states(max_steps):
     """the ring tape of a pipelined value-and-grad kernel: the smallest power of two >= max_steps + 2 states"""
     T = 1

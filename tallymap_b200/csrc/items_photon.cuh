@@ -39,7 +39,8 @@
 //
 // Buffers:
 //   ph_fwd   keys u32[N,2], mu_a f32, mu_s f32, consts i32[1], order | dep f32[64^3], dep accumulator f64[64^3], ctl,
-//            stats | k i32[N], trunc u8[N]   (the deposits accumulate in f64, rounded once to dep by the epilogue)
+//            stats | k i32[N], trunc u8[N]   (the deposits accumulate in f64 -- the 16^3 voxels around the source
+//            first per block in a shared f32 window -- and are rounded once to dep by the epilogue)
 //   ph_grad  keys, mu_a, mu_s, ct_dep f32[64^3], consts i32[3], order | g f32[2], exact u64[11], ctl, stats |
 //            trunc u8[N], replay scratch (stored state: p, d, w; the counters are the step index, alive is true)
 #pragma once
@@ -91,7 +92,9 @@ struct PhotonCommon {
 
 struct PHFwd : PhotonCommon {
   enum { kKeys, kMuA, kMuS, kConsts, kOrder, kDep, kDep64, kCtl, kStats, kK, kTrunc, kNBuf };
-  static constexpr int kSmemBytes = 0;
+  // the shared-memory window of hot voxels: x, y in [32 - kW/2, 32 + kW/2), z in [0, kW) (the source is (32, 32, 0))
+  static constexpr int kW = 16, kW0 = 32 - kW / 2;
+  static constexpr int kSmemBytes = kW * kW * kW * 4;
   struct Ctx {
     const uint2* keys;
     float mu_t, albedo, frac;
@@ -102,9 +105,11 @@ struct PHFwd : PhotonCommon {
     i32* kout;
     uint8_t* trunc;
     Key key;
+    float* win;
   };
   typedef PhotonState State;
-  __device__ static void setup(Ctx& c, const Params& P, unsigned char*) {
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.win = reinterpret_cast<float*>(smem);
     c.keys = static_cast<const uint2*>(P.p[kKeys]);
     const float mu_a = __ldg(static_cast<const float*>(P.p[kMuA]));
     const float mu_s = __ldg(static_cast<const float*>(P.p[kMuS]));
@@ -132,8 +137,11 @@ struct PHFwd : PhotonCommon {
     s.py = s.py + sl * s.dy;
     s.pz = s.pz + sl * s.dz;
     const bool inside = in_box(s.px) && in_box(s.py) && in_box(s.pz);
-    const i32 flat = (voxel(s.px) * kBox + voxel(s.py)) * kBox + voxel(s.pz);
-    datom_warp(c.dep64, flat, inside ? s.w * c.frac : 0.0f);
+    const i32 ix = voxel(s.px), iy = voxel(s.py), iz = voxel(s.pz);
+    const i32 flat = (ix * kBox + iy) * kBox + iz;
+    const bool in_win = (u32)(ix - kW0) < (u32)kW && (u32)(iy - kW0) < (u32)kW && iz < kW;
+    const i32 widx = in_win ? ((ix - kW0) * kW + (iy - kW0)) * kW + iz : -1;
+    datom_warp_window(c.dep64, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
     const float w1 = s.w * c.albedo;
     scatter(s, u.u1, u.u2);
     const bool low = w1 < 0.001f, survive = u.u3 < 0.1f;
@@ -146,7 +154,15 @@ struct PHFwd : PhotonCommon {
     c.kout[item] = s.k;
     c.trunc[item] = (s.kc >= c.M && s.alive) ? 1 : 0;
   }
-  __device__ static void flush(const Ctx&, const unsigned char*, int, int) {}
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    const float* win = reinterpret_cast<const float*>(smem);
+    for (int b = tid; b < kW * kW * kW; b += nth) {
+      const float v = win[b];
+      if (v == 0.0f) continue;
+      const int ix = kW0 + b / (kW * kW), iy = kW0 + (b / kW) % kW, iz = b % kW;
+      atomicAdd(&c.dep64[(ix * kBox + iy) * kBox + iz], (double)v);
+    }
+  }
   __device__ static void epilogue(const Ctx& c, int tid, int nth) { f64_to_f32(c.dep64, c.dep, kS, tid, nth); }
 };
 

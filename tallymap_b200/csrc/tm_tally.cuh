@@ -136,6 +136,32 @@ __device__ __forceinline__ void datom_warp(double* base, i32 idx, float v) {
   if (lane == __ffs(peers) - 1) atomicAdd(&base[idx], sum);
 }
 
+// datom_warp with a shared-memory window: when widx >= 0 (a function of idx: every lane of a group has the same) the
+// group's sum goes to the block's f32 window bin widx instead of the global f64 bin idx.  The window holds the hot
+// bins (a photon's first deposits land next to the source), so most adds are shared-memory atomics; the block adds
+// its window into the f64 bins once, at its flush.  Per block a window bin sums a few thousand values in f32
+// (relative error ~1e-6), and the f64 total over the blocks rounds once.
+__device__ __forceinline__ void datom_warp_window(double* base, float* win, i32 idx, i32 widx, float v) {
+  const unsigned active = __activemask();
+  const int lane = threadIdx.x & 31;
+  const bool live = v != 0.0f;
+  const unsigned peers = __match_any_sync(active, live ? idx : -1 - lane);
+  if (!live) return;
+  double sum = (double)v;
+  if (peers != (1u << lane)) {
+    sum = 0.0;
+    unsigned rest = peers;
+    while (rest) {
+      const int src = __ffs(rest) - 1;
+      rest &= rest - 1u;
+      sum = sum + (double)__shfl_sync(peers, v, src);
+    }
+    if (lane != __ffs(peers) - 1) return;
+  }
+  if (widx >= 0) atomicAdd(&win[widx], (float)sum);
+  else atomicAdd(&base[idx], sum);
+}
+
 // the epilogue of an f64-accumulated tally: out[i] = f32(acc[i]) (round to nearest), block-wide
 __device__ __forceinline__ void f64_to_f32(const double* acc, float* out, int n, int tid, int nth) {
   for (int i = tid; i < n; i += nth) out[i] = __double2float_rn(acc[i]);
