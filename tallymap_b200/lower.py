@@ -75,6 +75,12 @@ def c_expr(e, a):
         return f"({a[0]} {op} {a[1]})" if d != T.BOOL else f"({a[0]} {op} {a[1]})"
     if p == "not":
         return f"(!{a[0]})" if d == T.BOOL else f"(~{a[0]})"
+    if p == "shl":      # (a shift by 32 or more gives 0, as lax.shift_left; C would leave it undefined)
+        return f"((u32)({a[1]}) >= 32u ? ({CTYPE[d]})0 : ({CTYPE[d]})((u32)({a[0]}) << (u32)({a[1]})))"
+    if p == "shr":      # logical for u32, arithmetic for i32; 32 or more: 0, or the sign for i32
+        if d == T.U32:
+            return f"((u32)({a[1]}) >= 32u ? 0u : ({a[0]} >> (u32)({a[1]})))"
+        return f"((u32)({a[1]}) >= 32u ? ({a[0]} < 0 ? (i32)-1 : (i32)0) : ({a[0]} >> (u32)({a[1]})))"
     if p in _MATH:
         return f"{_MATH[p]}({a[0]})"
     if p == "sqrt":

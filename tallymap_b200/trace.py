@@ -181,6 +181,17 @@ class Var:
     def __xor__(self, o):
         return _binary("xor", self, o)
 
+    def __lshift__(self, o):
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: << on integers only")
+        return _binary("shl", self, o)
+
+    def __rshift__(self, o):
+        """logical for uint32, arithmetic for int32 (lax.shift_right_logical / _arithmetic)"""
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: >> on integers only")
+        return _binary("shr", self, o)
+
     def __invert__(self):
         return _cur().emit("not", [self], [self.dtype])[0]
 

@@ -61,3 +61,24 @@ def walk_records(t, x, key, drift):
     k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
     t = t.append("exit", {"k": k, "side": (x > 1).astype(tl.int32)})
     return t, k
+
+
+def edges(t, a, key, n, s):
+    """every lowered primitive on awkward values (NaN, +-inf, -0, huge, negative integers), its results recorded so
+    that they compare bitwise: a fixed number n of steps per item"""
+    def body(c):
+        k, x, t = c
+        kk = tl.random.fold_in(key, k)
+        u = tl.random.uniform(kk)
+        b = tl.random.bits(kk, (2,))
+        xi = x.astype(tl.int32)
+        q = (xi - 7) // 3
+        r = (xi - 7) % 3
+        y = tl.where(x > 0.5, tl.log(x), tl.exp(-x * s)) + tl.power(u + 0.5, s)
+        z = tl.minimum(tl.maximum(tl.sin(x * u), -0.0), tl.abs(tl.cos(y))) - tl.floor(x * 0.3) + tl.sqrt(u)
+        t = t.append("rec", {"i": xi, "q": q, "r": r, "b": (b[0] ^ (b[1] >> 3)).astype(tl.int32), "y": y, "z": z,
+                             "u": (x * 1e30).astype(tl.uint32).astype(tl.int32)})
+        t = t.add("h", (q % 8,), 1)
+        return k + 1, x * (1.5 - u) - 3.0 * s, t
+    k, x, t = tl.while_loop(lambda c: c[0] < n, body, (0, a, t))
+    return t, k

@@ -109,3 +109,23 @@ def test_records_lower_and_compile():
     assert "atomicAdd(c.r0ctr, 1ull)" in L.fwd_source
     with pytest.raises(NotImplementedError):
         L.grad_program((0,))
+
+
+def test_ir_evaluator_matches_the_oracle(orc):
+    """the IR evaluator (the lowering's oracle) against the hand-written oracle on the traced walk and quickstart"""
+    from oracle.ir_eval import Evaluator
+    kx, ks = prng.split(prng.PRNGKey(1), 2)
+    x, k = prng.uniform(kx, 40), prng.split(ks, 40)
+    tr = T.trace_item(walk, ["f32", "key", "f32"], 2, {"hist": ((256,), "f32"), "side": ((2,), "f32")})
+    r = Evaluator(tr, 20000).run([x, k], [1.0])
+    ref = orc.rw_fwd(x, k, 1.0)
+    assert np.array_equal(r["results"][0], ref["k"]) and np.array_equal(r["trunc"], ref["trunc"])
+    assert np.array_equal(r["stats"], ref["stats"])
+    assert np.abs(r["sums"]["hist"] - ref["hist"]).max() <= 1e-6 * np.abs(ref["hist"]).max()
+    xq = np.linspace(0.1, 0.99, 50, dtype=np.float32)
+    kq = prng.split(prng.PRNGKey(0), 50)
+    trq = T.trace_item(quickstart, ["f32", "key", "f32"], 2, {"hist": ((16,), "f32")})
+    rq = Evaluator(trq, 100).run([xq, kq], [2.0])
+    refq = orc.q1_fwd(xq, kq, 2.0)
+    assert np.array_equal(rq["results"][0], refq["k"])
+    assert np.abs(rq["sums"]["hist"] - refq["hist"]).max() <= 1e-6 * np.abs(refq["hist"]).max()

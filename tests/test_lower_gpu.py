@@ -238,3 +238,64 @@ def test_records_overflow_poisons(cuda):
     assert int(r.stats["records_dropped"]["hits"]) == int(r.stats["appended"]["hits"]) - 8 > 0
     assert (r.outputs["hits"]["k"].cpu().numpy() == -1).all() and torch.isnan(r.outputs["hits"]["x"]).all()
     assert torch.isnan(r.outputs["hist"]).all()
+
+
+def _eval(fn, in_specs, npi, specs, records, args, M, exact=()):
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as Tr
+    tr = Tr.trace_item(fn, in_specs, npi, specs, records)
+    return Evaluator(tr, M, exact).run(list(args[:npi]), list(args[npi:]))
+
+
+def test_lowered_against_ir_evaluator_edges(cuda):
+    """every primitive on awkward values, bitwise (through Records), against the IR evaluator"""
+    from items_lang import edges
+    vals = np.float32([np.nan, np.inf, -np.inf, -0.0, 0.0, 1e38, -1e38, 3e-39, -7.5, 7.5, 0.6, 123456.0, -2.0, 0.25])
+    n = len(vals)
+    keys = prng.split(prng.PRNGKey(21), n)
+    steps = np.full(n, 3, np.int32)
+    args = (vals, keys, steps, np.float32(0.7))
+    fields = {"i": torch.int32, "q": torch.int32, "r": torch.int32, "b": torch.int32, "y": torch.float32,
+              "z": torch.float32, "u": torch.int32}
+    outs = {"h": tm.Sum((8,), torch.int32), "rec": tm.Records(fields, capacity=256)}
+    f = tm.vmap(edges, outputs=outs, in_axes=(0, 0, 0, None), max_steps=10)
+    r = f(*args)
+    torch.cuda.synchronize()
+    recspec = {"rec": (256, tuple((k, "f32" if v == torch.float32 else "i32") for k, v in sorted(fields.items())))}
+    ref = _eval(edges, ["f32", "key", "i32", "f32"], 3, {"h": ((8,), "i32")}, recspec, args, 10)
+    m = len(ref["records"]["rec"])
+    assert m == 3 * n and int(r.stats["appended"]["rec"]) == m
+    got = {k: v.cpu().numpy() for k, v in r.outputs["rec"].items()}
+    for j, (fname, _) in enumerate(recspec["rec"][1]):
+        want = np.array([rec[j] for rec in ref["records"]["rec"]])
+        g = got[fname][:m]
+        if g.dtype == np.float32:
+            w = want.astype(np.float32)
+            # bitwise, NaN payloads aside (the device's canonical NaN and the host's differ in sign and payload)
+            same = (g.view(np.uint32) == w.view(np.uint32)) | (np.isnan(g) & np.isnan(w))
+            assert same.all() and np.isnan(w).sum() > 0, fname
+        else:
+            assert np.array_equal(g.astype(np.int64), want.astype(np.int64)), fname
+    assert np.array_equal(r.outputs["h"].cpu().numpy(), ref["sums"]["h"])
+
+
+def test_lowered_against_ir_evaluator_fixed_point_and_records(cuda):
+    from items_lang import walk_records
+    n = 400
+    x, k = rw_inputs(n, seed=17)
+    outs = {"hist": tm.Sum((256,), fixed_point=True),
+            "hits": tm.Records({"k": torch.int32, "x": torch.float32}, capacity=1 << 16),
+            "exit": tm.Records({"k": torch.int32, "side": torch.int32}, capacity=n)}
+    f = tm.vmap(walk_records, outputs=outs, in_axes=(0, 0, None), max_steps=20000)
+    r = f(x, k, np.float32(1.0))
+    torch.cuda.synchronize()
+    recs = {"hits": (1 << 16, (("k", "i32"), ("x", "f32"))), "exit": (n, (("k", "i32"), ("side", "i32")))}
+    ref = _eval(walk_records, ["f32", "key", "f32"], 2, {"hist": ((256,), "f32")}, recs, (x, k, np.float32(1.0)),
+                20000, exact=("hist",))
+    assert np.array_equal(bits(r.outputs["hist"].cpu().numpy()), bits(ref["sums"]["hist"]))
+    m = len(ref["records"]["hits"])
+    hk = np.array([h[0] for h in ref["records"]["hits"]], np.int32)
+    hx = np.array([h[1] for h in ref["records"]["hits"]], np.float32)
+    assert np.array_equal(r.outputs["hits"]["k"].cpu().numpy()[:m], hk)
+    assert np.array_equal(bits(r.outputs["hits"]["x"].cpu().numpy()[:m]), bits(hx))
+    assert np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
