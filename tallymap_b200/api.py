@@ -1,17 +1,21 @@
-"""The user-facing layer over the backend: `vmap(item, outputs, in_axes, max_steps)` returning `Result`, and the
-reverse-mode gradient of a mapped call with respect to a broadcast operand, with the reference's result contract
+"""The user-facing layer over the backend: `vmap(item, outputs, in_axes, max_steps)` returning `Result`, its
+reverse mode (`grad`, `value_and_grad`) and forward mode (`jvp`, `jacfwd`), with the reference's result contract
 (tallymap/_api.py:180-195, 681-698, 898-958):
 
-  * outputs: the summed tallies; EVERY float output is NaN when a resource limit intervened (an item hit
-    max_steps, counted in stats['n_truncated']); integer outputs and per-item results are never poisoned;
+  * outputs: the Sums (and Records); EVERY float output is NaN when a resource limit intervened (an item hit
+    max_steps, counted in stats['n_truncated']; a Records output overflowed); integer outputs and per-item results
+    are never poisoned;
   * per_item: the item's per-item results; truncated: bool[N];
-  * stats: spawned, children_dropped, children_truncated, fixed_point_overflow, dropped_emits, n_truncated.
+  * stats: spawned, children_dropped, children_truncated, fixed_point_overflow, dropped_emits, n_truncated (and
+    appended / records_dropped for Records).
 
-A gradient is ONE replay launch (the adjoint program recomputes every item from its inputs: _api.py:951-958) whose
-own truncation flags poison the cotangent (_primitive.py:586-594).
+A gradient is a replay launch (the adjoint program recomputes every item from its inputs: _api.py:951-958) whose own
+truncation flags poison the cotangent (_primitive.py:586-594); `value_and_grad` with cotangents given up front is one
+fused launch where the item has a pipelined value-and-grad program; through spawn it is the tree adjoint.
 
-Items are lowered programs (backend.ItemProgram families).  JAX is not a dependency: an item is named by its
-program family rather than traced from a Python function.
+An item is either a Python function written against tallymap_b200.lang -- traced, lowered to CUDA and compiled on
+its first call (MappedFn) -- or the name of a hand-lowered family ("quickstart", "walk1d", "photon", "lorenz",
+"shower": Mapped).  JAX is not a dependency.
 """
 import dataclasses
 from typing import Any, NamedTuple

@@ -8,6 +8,10 @@ first n_zero of them, launches through the C ABI on the current CUDA stream, and
 order (backends/kernel/__init__.py:177-185, _primitive._abstract): [sum tallies] + [stats] + [per-item results].
 Keys enter as uint32[..., 2] key data (__init__.py:131-132).
 
+Also here: replay_plan (the replay's checkpoint count C, sized from device memory), tree_grad (reverse mode through
+spawn: the recording forward, the generation lists and one adjoint launch per generation) and canonical_records (the
+Records layout after a launch).
+
 Everything runs on the GPU through libtm_b200.so; there is no CPU path.  Device memory and streams come from torch.
 """
 import dataclasses
