@@ -299,3 +299,20 @@ def test_lowered_against_ir_evaluator_fixed_point_and_records(cuda):
     assert np.array_equal(r.outputs["hits"]["k"].cpu().numpy()[:m], hk)
     assert np.array_equal(bits(r.outputs["hits"]["x"].cpu().numpy()[:m]), bits(hx))
     assert np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
+
+
+def test_quickstart_grad_and_jvp_agree(cuda):
+    """the reference's quickstart check (examples/quickstart.py:43-53): for loss = sum(hist ** 2), reverse mode
+    (a replay with the cotangent 2 hist, taken from the forward) and forward mode (2 <hist, d hist / d theta>) agree
+    to 1e-4"""
+    n = 10000
+    x = np.linspace(0.1, 0.99, n, dtype=np.float32)
+    k = prng.split(prng.PRNGKey(0), n)
+    f = tm.vmap(quickstart, outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=100)
+    r = f(x, k, np.float32(2.0))
+    hist = r.outputs["hist"]
+    g = float(f.grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": 2.0 * hist}))
+    _, d = f.jvp(x, k, np.float32(2.0), wrt=2, tangents=[1.0])
+    t = float(2.0 * (hist.double() * d["hist"].double()).sum())
+    assert int(r.stats["n_truncated"]) == 0
+    assert abs(g - t) <= 1e-4 * abs(t)
