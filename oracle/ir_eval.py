@@ -14,7 +14,10 @@ device:
   * emits: an index outside the output is dropped and counted in stats[4]; f32 Sums accumulate in f64 (the checker
     mode: compare within the float-tally tolerance), int32 Sums exactly, fixed_point f32 Sums through the oracle's
     exact accumulator (oracle.exact_sum, pinned to the golden known answers: compare bitwise);
-  * Records: each item's records in append order, items in item order (the canonical layout).
+  * Records: each item's records in append order, items in item order (the canonical layout);
+  * spawn (tallymap/_tally.py:284-302): a spawned child runs the same item from its leaves with the same broadcast
+    operands, after the roots, first in first out (no queue limit); its per-item results are discarded, its
+    truncation counts in stats[2], every spawn in stats[0].
 """
 import math
 
@@ -189,8 +192,8 @@ def _lit(x):
 class Evaluator:
     """evaluate traced item `tr` over items: run(per_item operands, broadcast values) -> dict of outputs"""
 
-    def __init__(self, tr, max_steps, exact=()):
-        self.tr, self.M, self.exact = tr, int(max_steps), set(exact)
+    def __init__(self, tr, max_steps, exact=(), max_items=10 ** 7):
+        self.tr, self.M, self.exact, self.max_items = tr, int(max_steps), set(exact), max_items
 
     def _val(self, x, env):
         return env[x.id] if isinstance(x, T.Var) else _lit(x)
@@ -204,6 +207,10 @@ class Evaluator:
             if e.prim == "append":
                 if a[0]:
                     out["appends"].append((e.params["records"], tuple(a[1:])))
+                continue
+            if e.prim == "spawn":
+                if a[0]:
+                    out["spawns"].append(tuple(a[1:]))
                 continue
             r = _eval(e, a)
             if len(e.outs) == 1:
@@ -227,6 +234,10 @@ class Evaluator:
         results = [np.zeros(n, np.int64 if (isinstance(y, T.Var) and y.dtype != T.F32) or
                             (isinstance(y, T.Lit) and y.dtype != T.F32) else np.float32) for y in tr.results]
         trunc = np.zeros(n, bool)
+        leaves_of = []                    # the per-item input variables, flattened as a child carries them
+        for x in tr.inputs[:tr.n_per_item]:
+            leaves_of += [x.a, x.b] if isinstance(x, T.Key) else (list(x) if isinstance(x, tuple) else [x])
+        work = []
         for i in range(n):
             env = {}
             for x, col in zip(tr.inputs[:tr.n_per_item], per_item):
@@ -238,9 +249,15 @@ class Evaluator:
                         env[xj.id] = F32(vj) if xj.dtype == T.F32 else int(vj)
                 else:
                     env[x.id] = F32(v) if x.dtype == T.F32 else int(v)
+            work.append((i, env))
+        w = 0
+        while w < len(work):
+            i, env = work[w]
+            work[w] = None
+            w += 1
             for x, v in zip(tr.inputs[tr.n_per_item:], bc):
                 env[x.id] = F32(v) if x.dtype == T.F32 else int(v)
-            out = {"emits": [], "appends": []}
+            out = {"emits": [], "appends": [], "spawns": []}
             self._run_eqns(tr.pre, env, out)
             carry = [self._val(x, env) for x in tr.carry_in]
             kc = 0
@@ -256,12 +273,21 @@ class Evaluator:
                 self._run_eqns(tr.body, env, out)
                 carry = [self._val(x, env) for x in tr.body_out]
                 kc += 1
-            trunc[i] = kc >= self.M and pred(carry)
+            tr_i = kc >= self.M and pred(carry)
             for v, x in zip(tr.post_carry, carry):
                 env[v.id] = x
             self._run_eqns(tr.post, env, out)
-            for r, y in enumerate(tr.results):
-                results[r][i] = self._val(y, env)
+            if i is None:
+                stats[2] += int(tr_i)
+            else:
+                trunc[i] = tr_i
+                for r, y in enumerate(tr.results):
+                    results[r][i] = self._val(y, env)
+            for ch in out["spawns"]:
+                stats[0] += 1
+                work.append((None, {x.id: v for x, v in zip(leaves_of, ch)}))
+            if self.max_items and len(work) > self.max_items:
+                raise RuntimeError("ir_eval: the spawn tree outgrew max_items")
             for nm, idx, v in out["emits"]:
                 S = len(sums[nm])
                 if not 0 <= idx < S:

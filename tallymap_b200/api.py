@@ -3,8 +3,9 @@ reverse mode (`grad`, `value_and_grad`) and forward mode (`jvp`, `jacfwd`), with
 (tallymap/_api.py:180-195, 681-698, 898-958):
 
   * outputs: the Sums (and Records); EVERY float output is NaN when a resource limit intervened (an item hit
-    max_steps, counted in stats['n_truncated']; a Records output overflowed); integer outputs and per-item results
-    are never poisoned;
+    max_steps, counted in stats['n_truncated']; a spawned child hit max_steps or did not fit the Queue, counted in
+    stats['children_truncated'] / ['children_dropped']; a Records output overflowed: _api.py:898-915); integer
+    outputs and per-item results are never poisoned;
   * per_item: the item's per-item results; truncated: bool[N];
   * stats: spawned, children_dropped, children_truncated, fixed_point_overflow, dropped_emits, n_truncated (and
     appended / records_dropped for Records).
@@ -40,6 +41,20 @@ class Sum:
         object.__setattr__(self, "shape", tuple(int(s) for s in self.shape))
         if self.fixed_point and self.dtype != torch.float32:
             raise NotImplementedError("tallymap_b200: fixed_point Sums of float32 only (the exact accumulator)")
+
+
+@dataclasses.dataclass(frozen=True)
+class Queue:
+    """the spawn queue of a spawning item (tallymap.Queue, _api.py:88-98): a ring of `capacity` slots for children
+    shared between threads.  Each thread runs the children it spawns depth-first from a private stack and shares
+    through the ring only what idle threads wait for, so the ring holds at most about one child per idle thread; a
+    child that finds it full is dropped, counted in stats['children_dropped'], and poisons every float output."""
+    capacity: int
+
+    def __post_init__(self):
+        if not 1 <= int(self.capacity) <= 2 ** 31 - 1:
+            raise ValueError("tallymap_b200.Queue: capacity in [1, 2^31 - 1]")
+        object.__setattr__(self, "capacity", int(self.capacity))
 
 
 @dataclasses.dataclass(frozen=True)
@@ -96,6 +111,15 @@ FAMILIES = {
 }
 
 
+def _limits(p, stats):
+    """did a resource limit intervene (_api.py:898-912, _limits)?  An item hit max_steps; for a spawning program
+    also a child that did not fit the queue or hit max_steps.  -> a bool tensor on the device"""
+    bad = stats["n_truncated"] > 0
+    if p.spawns:
+        bad = bad | (stats["children_dropped"] > 0) | (stats["children_truncated"] > 0)
+    return bad
+
+
 def _poison(outs, bad):
     """NaN for every float output when `bad` (a select, so a clean call is bitwise unchanged: _api.py:916-925)."""
     return {n: (torch.where(bad, torch.full_like(v, float("nan")), v) if v.is_floating_point() else v)
@@ -105,8 +129,11 @@ def _poison(outs, bad):
 class Mapped:
     """tallymap.vmap(item, outputs, in_axes, max_steps) over a lowered item family."""
 
-    def __init__(self, fam, outputs, in_axes, max_steps):
+    def __init__(self, fam, outputs, in_axes, max_steps, spawn=None):
         self.fam = fam
+        if spawn is not None and not fam.fwd.spawns:
+            raise ValueError(f"tallymap_b200: item {fam.name!r} does not spawn")
+        self.queue = spawn.capacity if spawn is not None else None
         names = [t.name for t in fam.fwd.tallies]
         if sorted(outputs) != sorted(names):
             raise KeyError(f"tallymap_b200: item {fam.name!r} writes outputs {names}, got {sorted(outputs)}")
@@ -131,7 +158,7 @@ class Mapped:
     def __call__(self, *args):
         pi, bc = self._split(args)
         p = self.fam.fwd
-        out = B.run(p, pi, bc, consts=(self.max_steps,))
+        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.queue)
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
@@ -141,7 +168,7 @@ class Mapped:
         n_tr = trunc.sum(dtype=torch.int32)
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
-        outs = _poison(tallies, n_tr > 0)
+        outs = _poison(tallies, _limits(p, stats))
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
     def value_and_grad(self, *args, wrt, cotangents, fused=True):
@@ -264,8 +291,11 @@ class MappedFn:
     operand signature, lowered to CUDA and compiled for sm_100a at run time (tallymap_b200.lower, NVRTC); the reverse
     programs are lowered and compiled on the first gradient request for each set of differentiated operands."""
 
-    def __init__(self, fn, outputs, in_axes, max_steps):
+    def __init__(self, fn, outputs, in_axes, max_steps, spawn=None):
         self.fn = fn
+        if spawn is not None and not isinstance(spawn, Queue):
+            raise TypeError("tallymap_b200: spawn= takes a tallymap_b200.Queue(capacity)")
+        self.spawn = spawn
         self.outputs = {}
         for name, o in outputs.items():
             if isinstance(o, Records):
@@ -318,7 +348,7 @@ class MappedFn:
                     args_[pos] = x
                 return self.fn(t, *args_)
             item.__name__ = getattr(self.fn, "__name__", "item")
-            self._lowered[key] = lower.Lowered(item, pis + bcs, len(pis), self.outputs)
+            self._lowered[key] = lower.Lowered(item, pis + bcs, len(pis), self.outputs, spawn=self.spawn is not None)
         self.last_lowered = self._lowered[key]
         return self._lowered[key]
 
@@ -331,7 +361,7 @@ class MappedFn:
         L = self.lowered(args)
         pi, bc = self._split(args)
         p = L.fwd
-        out = B.run(p, pi, bc, consts=(self.max_steps,))
+        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.spawn.capacity if self.spawn else None)
         raw = B.run.last["results"]
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
@@ -342,7 +372,7 @@ class MappedFn:
         n_tr = trunc.sum(dtype=torch.int32)
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
-        bad = n_tr > 0
+        bad = _limits(p, stats)
         if p.records:
             counts = {nm: ys[L.n_results + r] for r, (nm, _, _) in enumerate(p.records)}
             recs = B.canonical_records(p, raw, counts)
@@ -434,11 +464,11 @@ class MappedFn:
         return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
 
 
-def vmap(item, outputs, in_axes, max_steps=None):
+def vmap(item, outputs, in_axes, max_steps=None, spawn=None):
     """tallymap.vmap: `item` is a Python function written against tallymap_b200.lang (traced, lowered and compiled
     on first call) or the name of a built-in lowered family ("quickstart", "walk1d", "photon", "lorenz",
-    "shower")."""
+    "shower").  spawn: a Queue, for an item that spawns children with t.spawn (_api.py:88-98, 426-433)."""
     if callable(item) and not isinstance(item, Family):
-        return MappedFn(item, outputs, in_axes, max_steps)
+        return MappedFn(item, outputs, in_axes, max_steps, spawn)
     fam = FAMILIES[item] if isinstance(item, str) else item
-    return Mapped(fam, outputs, in_axes, max_steps)
+    return Mapped(fam, outputs, in_axes, max_steps, spawn)

@@ -73,8 +73,15 @@ __device__ __forceinline__ bool wait_seq(const u32* seq, u32 slot, u32 want) {
 //   start_child(Ctx&, const Child&) -> State       a popped child's pre-loop code
 //   step(const Ctx&, State&, Child& o0, Child& o1, int& n_out)   one step; up to 2 children to spawn
 //   finish(const Ctx&, const State&, i64 item, bool child)   post-loop code; per-item results for roots only
+// or, with kPostSpawn = true (children spawned after the loop, tallymap/_tally.py spawn in the post-loop code):
+//   finish(const Ctx&, const State&, i64 item, bool child, Child& o0, Child& o1, int& n_out)
+template <class T, class = void>
+struct post_spawn_trait : tmstd::false_type {};
+template <class T>
+struct post_spawn_trait<T, tmstd::void_t<decltype(T::kPostSpawn)>> : tmstd::integral_constant<bool, T::kPostSpawn> {};
+
 template <class I>
-__global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i64 n_items) {
+__device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
   typename I::Ctx cx;
   I::setup(cx, P, smem);
@@ -213,6 +220,7 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
         I::step(cx, x, o0, o1, n_out);
       } else {
         done = true;
+        if constexpr (post_spawn_trait<I>::value) I::finish(cx, x, item, child, o0, o1, n_out);
       }
     }
     // ---- spawned children: onto the private stack unless lanes are hungry for them (or the stack is full), else
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
       if (lane == leader && warp_pub) atomicAdd(qword(q, kQPending), warp_pub);
     }
     if (done) {
-      I::finish(cx, x, item, child);
+      if constexpr (!post_spawn_trait<I>::value) I::finish(cx, x, item, child);
       active = false;
       if (ns == 0) {                 // busy -> idle: leave the in-flight count
         __threadfence();
@@ -290,6 +298,11 @@ __global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i
   __syncthreads();
   I::flush(cx, smem, threadIdx.x, blockDim.x);
   finish_block<I>(cx, ctl);
+}
+
+template <class I>
+__global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i64 n_items) {
+  spawn_body<I>(P, n_items);
 }
 
 }  // namespace tmb

@@ -192,6 +192,11 @@ class Item:
             else:
                 self.loads.append((x, f"__ldg(&c.in{j}[item])"))
         self.bc_ids = {b.id: k for k, b in enumerate(self.bc)}
+        # spawning items (tallymap/_tally.py spawn): a child carries the per-item input leaves, in load order
+        self.spawns = any(e.prim == "spawn" for e in tr.body + tr.post)
+        self.post_spawns = any(e.prim == "spawn" for e in tr.post)
+        if self.spawns and tr.records:
+            raise NotImplementedError("tallymap_b200: Records outputs of a spawning item are not lowered")
         # step counters: carries that start at 0 and gain 1 per step equal the step index (not stored by the replay)
         self.counter = set()
         by_id = {o.id: e for e in tr.body for o in e.outs}
@@ -230,11 +235,23 @@ def _names_loop(it, carry, state="s"):
     return n
 
 
-def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None):
+def _spawn_code(when_c, leaves_c):
+    """one spawn: the next of the step's two child slots (the spawn runtime's step interface)"""
+    st = [f"if ({when_c}) {{ Child& o_ = n_out == 0 ? o0 : o1;"]
+    st += [f" o_.l{m} = {v};" for m, v in enumerate(leaves_c)]
+    st.append(" ++n_out; }")
+    return "".join(st)
+
+
+def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None, spawner=None):
     """straight-line C for eqns; names: id -> C expression (updated with the locals defined here)"""
     out = []
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        if e.prim == "spawn":
+            if spawner is not None:
+                out.append(indent + spawner(a[0], a[1:]))
+            continue
         if e.prim == "append":
             if appender is not None:
                 out.append(indent + appender(e.params["records"], a[0], a[1:]))
@@ -264,8 +281,10 @@ def forward_source(it):
     """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes, tally layout)"""
     tr = it.tr
     npi, nbc = len(it.pi), len(it.bc)
-    lines = [PRELUDE, "namespace tmb {", "struct GenFwd {"]
-    # buffer indices: per-item, broadcast, consts, order | tallies, ctl, stats | ys, trunc
+    sp = it.spawns
+    lines = [('#include "tm_spawn.cuh"' if sp else "") + PRELUDE, "namespace tmb {", "struct GenFwd {"]
+    # buffer indices: per-item, broadcast, consts, order | tallies, [exact words], [records], [ring sequence and
+    # control words], ctl, stats | ys, [record counts], trunc, [ring]
     idx = 0
     enum = []
     for j in range(npi):
@@ -286,6 +305,9 @@ def forward_source(it):
         enum.append(f"kR{r}Cid = {idx}"); idx += 1
         enum.append(f"kR{r}K = {idx}"); idx += 1
         enum.append(f"kR{r}Ctr = {idx}"); idx += 1
+    if sp:
+        enum.append(f"kSeq = {idx}"); idx += 1
+        enum.append(f"kQctl = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
@@ -293,8 +315,17 @@ def forward_source(it):
     for r in range(len(recs)):
         enum.append(f"kR{r}N = {idx}"); idx += 1
     enum.append(f"kTrunc = {idx}"); idx += 1
+    if sp:
+        enum.append(f"kQueue = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
+    if sp:
+        # a child: the per-item input leaves (4 bytes each), in the order start() loads them
+        lines.append("  enum { kConstM, kConstQ };")
+        lines.append("  struct Child { " + " ".join(f"{CTYPE[v.dtype]} l{m};" for m, (v, _) in enumerate(it.loads))
+                     + " };")
+        if it.post_spawns:
+            lines.append("  static constexpr bool kPostSpawn = true;")
     # privatised tallies
     smem, priv = 0, {}
     for t, (name, (shape, dt)) in enumerate(it.specs):
@@ -401,43 +432,60 @@ def forward_source(it):
         return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
                 f"else if ({v_c}) atomicAdd(&{tgt}[b_], {v_c}); }}")
 
-    # start: inputs, pre-loop code, the saved values, the initial carry
-    lines.append("  __device__ static State start(Ctx& c, i64 item) {")
-    names = _names_pre(it)
-    for v, ld in it.loads:
-        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
-    lines += _emit_code(tr.pre, names, emitter)
-    for i in it.saved:
-        lines.append(f"    c.p{i} = {names[i]};")
-    if recs:
-        lines.append("    c.item = item;")
-    lines.append("    State s;")
-    lines.append("    s.kc = 0;")
-    for r in range(len(recs)):
-        lines.append(f"    s.a{r} = 0;")
-    for j, x in enumerate(tr.carry_in):
-        lines.append(f"    s.c{j} = {_ref(x, names)};")
-    lines.append("    return s;")
-    lines.append("  }")
+    # start: inputs, pre-loop code, the saved values, the initial carry (start_child: the same from a child's leaves)
+    for head, src in [("State start(Ctx& c, i64 item)", [ld for _, ld in it.loads])] + \
+            ([("State start_child(Ctx& c, const Child& ch)", [f"ch.l{m}" for m in range(len(it.loads))])]
+             if sp else []):
+        lines.append(f"  __device__ static {head} {{")
+        names = _names_pre(it)
+        for (v, _), ld in zip(it.loads, src):
+            lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+        lines += _emit_code(tr.pre, names, emitter)
+        for i in it.saved:
+            lines.append(f"    c.p{i} = {names[i]};")
+        if recs:
+            lines.append("    c.item = item;")
+        lines.append("    State s;")
+        lines.append("    s.kc = 0;")
+        for r in range(len(recs)):
+            lines.append(f"    s.a{r} = 0;")
+        for j, x in enumerate(tr.carry_in):
+            lines.append(f"    s.c{j} = {_ref(x, names)};")
+        lines.append("    return s;")
+        lines.append("  }")
     lines += _pred_fn(it)
     lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
     lines.append("    return s.kc < c.M && pred(c, s);")
     lines.append("  }")
-    lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
+    if sp:
+        lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, "
+                     "int& n_out) {")
+    else:
+        lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
     names = _names_loop(it, tr.carry)
-    lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"))
+    lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"), spawner=_spawn_code)
     lines += _assign_carry(it, names)
     lines.append("  }")
-    lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    if not sp:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    elif it.post_spawns:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child, Child& o0, "
+                     "Child& o1, int& n_out) {")
+    else:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {")
     names = _names_loop(it, tr.post_carry)
     for r in range(len(recs)):
         lines.append(f"    i32 a{r} = s.a{r};")
-    lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"))
+    lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"), spawner=_spawn_code)
+    if sp:
+        # a child's per-item results are discarded (tallymap/_tally.py:285-286); its truncation is counted
+        lines.append("    const bool tr_ = s.kc >= c.M && pred(c, s);")
+        lines.append("    if (child) { if (tr_) atomicAdd(&c.stats[kStChildrenTruncated], 1); return; }")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
     for r in range(len(recs)):
         lines.append(f"    c.r{r}n[item] = a{r};")
-    lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
+    lines.append("    c.trunc[item] = " + ("tr_ ? 1 : 0;" if sp else "(s.kc >= c.M && pred(c, s)) ? 1 : 0;"))
     lines.append("  }")
     lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
     for name, (t, S, dt, pv) in tinfo.items():
@@ -458,7 +506,7 @@ def forward_source(it):
     lines.append("};")
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
-    lines.append("  tmb::forward_body<tmb::GenFwd>(P, n);")
+    lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenFwd>(P, n);")
     lines.append("}")
     return "\n".join(lines), max(smem, 16)
 
@@ -859,14 +907,14 @@ class Lowered:
     """a traced item's programs: the forward (compiled at construction) and its reverse programs (compiled per set
     of differentiated broadcast operands, on first use)"""
 
-    def __init__(self, fn, in_specs, n_per_item, outputs, name=None):
+    def __init__(self, fn, in_specs, n_per_item, outputs, name=None, spawn=False):
         from .backend import ItemProgram, TSpec
         self.name = name or getattr(fn, "__name__", "item")
         recs = {k: (v[1], tuple(v[2])) for k, v in outputs.items() if v[0] == "records"}
         outputs = {k: v for k, v in outputs.items() if v[0] != "records"}
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
         exact = [k for k, v in outputs.items() if len(v) > 2 and v[2]]
-        self.tr = T.trace_item(fn, in_specs, n_per_item, specs, recs)
+        self.tr = T.trace_item(fn, in_specs, n_per_item, specs, recs, spawn=spawn)
         self.it = Item(self.tr, in_specs, self.name, exact)
         it = self.it
         src, smem = forward_source(it)
@@ -880,10 +928,13 @@ class Lowered:
         ys += (_operand("truncated", T.BOOL),)
         records = tuple((nm, int(cap), tuple((f, TDTYPE[dt]) for f, dt in fl)) for nm, (cap, fl) in recs.items())
         nrec = sum(len(fl) + 3 for _, _, fl in records)
-        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys)
+        sp = it.spawns
+        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys) + (3 if sp else 0)
         kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
-        self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc, consts=("max_steps",), tallies=tallies,
-                               ys=ys, trunc=len(ys) - 1, records=records)
+        self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc,
+                               consts=("max_steps", "queue") if sp else ("max_steps",), tallies=tallies,
+                               ys=ys, trunc=len(ys) - 1, records=records, spawns=sp,
+                               queue_leaf_bytes=4 * len(it.loads) if sp else 0)
         self.n_results = len(self.tr.results)
         self.grads = {}
         self.jvps = {}
@@ -900,6 +951,8 @@ class Lowered:
             if self.it.exact or self.fwd.records:
                 raise NotImplementedError("tallymap_b200: forward mode of fixed_point or Records outputs is not "
                                           "lowered")
+            if self.it.spawns:
+                raise NotImplementedError("tallymap_b200: forward mode through spawn is not lowered for traced items")
             src, smem = jvp_source(self.it, list(wrt), int(lanes))
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
@@ -917,6 +970,9 @@ class Lowered:
         wrt = tuple(wrt)
         if self.fwd.records:
             raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
+        if self.it.spawns:
+            raise NotImplementedError("tallymap_b200: reverse mode through spawn (the tree adjoint) is lowered for "
+                                      "the built-in shower only")
         if wrt not in self.grads:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:

@@ -226,9 +226,50 @@ class TallyToken:
     """the tally handle `t` of an item: t.add(name, index, value) records an emit, t.append(name, {field: value},
     when=...) a record; both return the handle"""
 
-    def __init__(self, specs, records=None):
+    def __init__(self, specs, records=None, child=None):
         self.specs = specs           # name -> (shape, dtype)
         self.records = records or {}  # name -> (capacity, ((field, dtype), ...) sorted by field)
+        self.child = child           # the per-item operands' specs: what a spawned child carries
+
+    def spawn(self, child, when=True):
+        """push a child item (tallymap/_tally.py:284-302, spawn): `child` holds its per-item operands with the
+        structure of the mapped per-item arguments (a tuple of them, in their order; a key as a key, a vector as a
+        tuple; one per-item argument may be given bare); it runs the same item function with the same broadcast
+        operands, and its per-item results are discarded"""
+        if self.child is None:
+            raise TraceError("tallymap_b200.lang: spawn needs a Queue (tallymap_b200.vmap(..., spawn=Queue(n)))")
+        if len(self.child) == 1 and not (isinstance(child, tuple) and len(child) == 1):
+            child = (child,)
+        if not isinstance(child, tuple) or len(child) != len(self.child):
+            raise TraceError(f"tallymap_b200.lang: a spawned child has the structure of the mapped per-item "
+                             f"arguments ({len(self.child)} of them)")
+        w = _lit(when)
+        if w.dtype != BOOL:
+            raise TraceError("tallymap_b200.lang: spawn's `when` must be a scalar bool")
+        leaves = []
+        for x, s in zip(child, self.child):
+            if s == "key":
+                if not isinstance(x, Key):
+                    raise TraceError("tallymap_b200.lang: a child's key operand must be a key")
+                leaves += [x.a, x.b]
+                continue
+            if isinstance(s, tuple):
+                if not isinstance(x, tuple) or len(x) != s[1]:
+                    raise TraceError(f"tallymap_b200.lang: a child's vector operand has {s[1]} elements")
+                xs, dt = x, s[0]
+            else:
+                xs, dt = (x,), s
+            for v in xs:
+                if isinstance(v, (Key, tuple)):
+                    raise TraceError("tallymap_b200.lang: a spawned child has the structure of the mapped inputs")
+                v = _lit(v)
+                if isinstance(v, Lit):
+                    v = Lit(float(v.value), F32) if dt == F32 else Lit(int(v.value), dt)
+                if v.dtype != dt:
+                    raise TraceError(f"tallymap_b200.lang: a child's operand is {dt}, got {v.dtype}")
+                leaves.append(v)
+        _cur().eqns.append(Eqn("spawn", [w] + leaves, [], {}))
+        return self
 
     def append(self, name, fields, when=True):
         """a Records output's append (tallymap/_tally.py:302-364): the fields of one record, written when `when`"""
@@ -394,7 +435,7 @@ def _flatten(tree):
     return leaves, rebuild
 
 
-def trace_item(fn, in_specs, n_per_item, specs, records=None):
+def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
     """trace item function `fn(t, *args)`; in_specs: per argument "f32" | "i32" | "u32" | "key" | ("f32", n)
     (a per-item vector); specs: Sum output name -> (shape, dtype); records: Records output name -> (capacity,
     ((field, dtype), ...)).  -> Traced"""
@@ -408,7 +449,7 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None):
             args.append(tuple(tr.new(s[0]) for _ in range(s[1])))
         else:
             args.append(tr.new(s))
-    tok = TallyToken(specs, records)
+    tok = TallyToken(specs, records, list(in_specs[:n_per_item]) if spawn else None)
     _CTX.append(tr)
     try:
         out = fn(tok, *args)
@@ -426,6 +467,10 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None):
     keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
     if any(e.prim == "append" for e in pre):
         raise TraceError("tallymap_b200.lang: append before the loop is not lowered (append in the loop or after it)")
+    if any(e.prim == "spawn" for e in pre):
+        raise TraceError("tallymap_b200.lang: spawn before the loop is not lowered (spawn in the loop or after it)")
+    if sum(e.prim == "spawn" for e in st["body"]) > 2 or sum(e.prim == "spawn" for e in post) > 2:
+        raise TraceError("tallymap_b200.lang: at most two spawns per loop step and two after the loop")
     return Traced(inputs=args, n_per_item=n_per_item, pre=pre, carry_in=[_lit(x) for x in keep(st["init"])],
                   carry=keep(st["carry"]), cond=st["cond"], cond_out=st["cond_out"], body=st["body"],
                   body_out=[_lit(x) for x in keep(st["body_out"])], post_carry=keep(st["post_carry"]), post=post,

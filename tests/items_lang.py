@@ -82,3 +82,36 @@ def edges(t, a, key, n, s):
         return k + 1, x * (1.5 - u) - 3.0 * s, t
     k, x, t = tl.while_loop(lambda c: c[0] < n, body, (0, a, t))
     return t, k
+
+
+def shower(t, E, depth, key, X0):
+    """BASELINE config 5's branching shower as a tallymap user writes it: one particle per item; a split particle
+    ends, replaced by two children spawned with the same per-item structure (energy, depth, key)"""
+    def body(c):
+        k, E, depth, alive, t = c
+        kk = tl.random.fold_in(key, k)
+        u = tl.random.uniform(kk, (3,))
+        depth = depth + X0 * -tl.log(1.0 - u[0])
+        low = E < 0.5
+        t = t.add("dep", tl.where(low, (depth * 8).astype(tl.int32), 0), tl.where(low, E, 0.0))
+        split = ~low & (u[1] < 0.7)
+        z = 0.1 + 0.8 * u[2]
+        t = t.spawn((E * z, depth, tl.random.fold_in(kk, 0)), when=split)
+        t = t.spawn((E * (1.0 - z), depth, tl.random.fold_in(kk, 1)), when=split)
+        return k + 1, E, depth, ~low & ~split, t
+    k, E, depth, alive, t = tl.while_loop(lambda c: c[3], body, (0, E, depth, True, t))
+    t = t.add("count", 0, 1)
+    return t, k
+
+
+def spawn_walk(t, g, x, key):
+    """a divergent walk that spawns one child (generation g + 1) AFTER its loop while g < 3 (the reference's
+    tests/invariants.py spawn_walk, with a random step): the post-loop spawn point"""
+    def body(c):
+        k, w, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        return k + 1, w * (0.5 + 0.5 * u), t.add("Q", k % 16, w).add("C", k % 16, 1)
+    n = 2 + g + (x > 1.0).astype(tl.int32)
+    k, w, t = tl.while_loop(lambda c: c[0] < n, body, (0, x, t))
+    t = t.spawn((g + 1, w * 1.25, tl.random.fold_in(key, 7)), when=g < 3)
+    return t, k

@@ -129,3 +129,70 @@ def test_ir_evaluator_matches_the_oracle(orc):
     refq = orc.q1_fwd(xq, kq, 2.0)
     assert np.array_equal(rq["results"][0], refq["k"])
     assert np.abs(rq["sums"]["hist"] - refq["hist"]).max() <= 1e-6 * np.abs(refq["hist"]).max()
+
+
+def _sh_specs():
+    return {"dep": ((512,), "f32"), "count": ((1,), "i32")}
+
+
+def test_spawn_traces_and_lowers():
+    """t.spawn lowers onto the spawn runtime: a Child of the per-item leaves, step with two child slots, a
+    start_child and the ring buffers; post-loop spawns take the finish form with child slots"""
+    from items_lang import shower, spawn_walk
+    tr = T.trace_item(shower, ["f32", "f32", "key", "f32"], 3, _sh_specs(), spawn=True)
+    assert sum(e.prim == "spawn" for e in tr.body) == 2 and len(tr.body[-1].ins) >= 1
+    f = tm.vmap(shower, outputs={"dep": tm.Sum((512,)), "count": tm.Sum((1,), tm.api.torch.int32)},
+                in_axes=(0, 0, 0, None), max_steps=100000, spawn=tm.Queue(4096))
+    from oracle import oracle as orc
+    E0, d0, keys = orc.sh_inputs(8)
+    L = f.lowered((E0, d0, keys, np.float32(1.0)))
+    assert L.fwd.spawns and L.fwd.queue_leaf_bytes == 16 and L.fwd.consts == ("max_steps", "queue")
+    src = L.fwd_source
+    assert "struct Child { float l0; float l1; u32 l2; u32 l3; };" in src
+    assert "start_child(Ctx& c, const Child& ch)" in src and "spawn_body<tmb::GenFwd>" in src
+    names = [n for n, _, _, _ in L.fwd.result_layout(8, queue=4096)[0]]
+    assert names == ["dep", "count", "queue.seq", "queue.ctl", "ctl", "stats", "y0", "truncated", "queue.ring"]
+    with pytest.raises(NotImplementedError):
+        L.grad_program((0,))
+    fw = tm.vmap(spawn_walk, outputs={"Q": tm.Sum((16,)), "C": tm.Sum((16,), tm.api.torch.int32)},
+                 in_axes=(0, 0, 0), max_steps=100, spawn=tm.Queue(1024))
+    Lw = fw.lowered((np.zeros(4, np.int32), np.ones(4, np.float32), prng.split(prng.PRNGKey(2), 4)))
+    assert "static constexpr bool kPostSpawn = true;" in Lw.fwd_source
+
+
+def test_spawn_trace_errors():
+    from items_lang import shower
+    with pytest.raises(T.TraceError, match="needs a Queue"):
+        T.trace_item(shower, ["f32", "f32", "key", "f32"], 3, _sh_specs())
+
+    def bad_structure(t, E, depth, key, X0):
+        def body(c):
+            k, t = c
+            t = t.spawn((E, key), when=k > 1)
+            return k + 1, t
+        k, t = tl.while_loop(lambda c: c[0] < 3, body, (0, t))
+        return t, k
+    with pytest.raises(T.TraceError, match="structure"):
+        T.trace_item(bad_structure, ["f32", "f32", "key", "f32"], 3, _sh_specs(), spawn=True)
+
+    def before_loop(t, E, depth, key, X0):
+        t = t.spawn((E, depth, key), when=E > 1.0)
+        k, t = tl.while_loop(lambda c: c[0] < 3, lambda c: (c[0] + 1, c[1]), (0, t))
+        return t, k
+    with pytest.raises(T.TraceError, match="before the loop"):
+        T.trace_item(before_loop, ["f32", "f32", "key", "f32"], 3, _sh_specs(), spawn=True)
+
+
+def test_ir_evaluator_shower_matches_the_oracle(orc):
+    """the evaluator runs spawned children: the traced shower against the hand-written oracle (particle count and
+    per-root trip counts bitwise, the deposit within the float-sum tolerance)"""
+    from items_lang import shower
+    from oracle.ir_eval import Evaluator
+    E0, d0, keys = orc.sh_inputs(6)
+    tr = T.trace_item(shower, ["f32", "f32", "key", "f32"], 3, _sh_specs(), spawn=True)
+    r = Evaluator(tr, 100000).run([E0, d0, keys], [1.0])
+    ref = orc.sh_fwd(E0, d0, keys, 1.0)
+    assert int(r["sums"]["count"][0]) == int(ref["count"][0])
+    assert np.array_equal(r["results"][0], ref["k"]) and np.array_equal(r["trunc"], ref["trunc"])
+    assert int(r["stats"][0]) == int(ref["stats"][0]) and int(r["stats"][4]) == int(ref["stats"][4])
+    assert np.abs(r["sums"]["dep"] - ref["dep"]).max() <= 1e-5 * np.abs(ref["dep"]).max()

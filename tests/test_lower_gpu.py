@@ -316,3 +316,83 @@ def test_quickstart_grad_and_jvp_agree(cuda):
     t = float(2.0 * (hist.double() * d["hist"].double()).sum())
     assert int(r.stats["n_truncated"]) == 0
     assert abs(g - t) <= 1e-4 * abs(t)
+
+
+# ---------------------------------------------------------------------------------------------- spawn
+def _shower_fn(Q=1 << 22, M=100000):
+    from items_lang import shower
+    return tm.vmap(shower, outputs={"dep": tm.Sum((512,)), "count": tm.Sum((1,), torch.int32)},
+                   in_axes=(0, 0, 0, None), max_steps=M, spawn=tm.Queue(Q))
+
+
+@pytest.mark.parametrize("n", [1, 777, 20000])
+def test_lowered_shower_matches_oracle(cuda, orc, n):
+    """the traced shower on the spawn runtime: particle count, spawned children, per-root trip counts, flags and
+    stats bitwise against the oracle; the deposit within the float-tally tolerance"""
+    E0, d0, keys = orc.sh_inputs(n)
+    r = _shower_fn()(E0, d0, keys, np.float32(1.0))
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    ref = orc.sh_fwd(E0, d0, keys, 1.0)
+    o = np_out(r)
+    assert np.array_equal(o["count"], ref["count"])
+    st = np.array([int(r.stats[s]) for s in B.STATS])
+    assert np.array_equal(st, ref["stats"]) and st[1] == 0
+    assert np.array_equal(r.per_item.cpu().numpy(), ref["k"])
+    assert np.array_equal(r.truncated.cpu().numpy(), ref["trunc"])
+    assert near(o["dep"], ref["dep"])
+
+
+def test_lowered_shower_matches_hand_lowered(cuda, orc):
+    """the traced shower against the hand-lowered SH_FWD kernel on 2^18 roots (~2.5e8 particles)"""
+    E0, d0, keys = orc.sh_inputs(1 << 18)
+    r = _shower_fn()(E0, d0, keys, np.float32(1.0))
+    torch.cuda.synchronize()
+    hand = B.run(B.SH_FWD, [E0, d0, keys], [np.float32(1.0)], consts=(100000,))
+    torch.cuda.synchronize()
+    o = np_out(r)
+    assert np.array_equal(o["count"], hand[1].cpu().numpy())
+    assert np.array_equal(r.per_item.cpu().numpy(), hand[3].cpu().numpy())
+    assert int(r.stats["spawned"]) == int(hand[2][0]) and int(r.stats["children_dropped"]) == 0
+    assert near(o["dep"], hand[0].cpu().numpy())
+
+
+def test_lowered_shower_small_queue_poisons(cuda, orc):
+    """a Queue too small for the children idle threads wait for: dropped children are counted and every float
+    output is NaN (_api.py:898-915); the integer count stays the particles that ran"""
+    E0, d0, keys = orc.sh_inputs(5000)
+    r = _shower_fn(Q=64)(E0, d0, keys, np.float32(1.0))
+    torch.cuda.synchronize()
+    dropped, spawned = int(r.stats["children_dropped"]), int(r.stats["spawned"])
+    assert dropped > 0
+    assert np.isnan(r.outputs["dep"].cpu().numpy()).all()
+    assert int(r.outputs["count"][0]) == 5000 + spawned
+
+
+@pytest.mark.parametrize("M", [100, 4])
+def test_lowered_post_loop_spawn_matches_evaluator(cuda, M):
+    """spawn after the loop (three generations of children); with max_steps = 4 the later generations truncate:
+    counted in stats['children_truncated'] and poisoning the float output, not the roots' flags"""
+    from items_lang import spawn_walk
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    n = 3000
+    rng = np.random.default_rng(9)
+    g = np.zeros(n, np.int32)
+    x = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(11), n)
+    f = tm.vmap(spawn_walk, outputs={"Q": tm.Sum((16,)), "C": tm.Sum((16,), torch.int32)}, in_axes=(0, 0, 0),
+                max_steps=M, spawn=tm.Queue(4096))
+    r = f(g, x, keys)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    tr = T.trace_item(spawn_walk, ["i32", "f32", "key"], 3, {"Q": ((16,), "f32"), "C": ((16,), "i32")}, spawn=True)
+    ref = Evaluator(tr, M).run([g, x, keys], [])
+    st = np.array([int(r.stats[s]) for s in B.STATS])
+    assert np.array_equal(st, ref["stats"]) and st[0] == 3 * n
+    assert np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
+    assert np.array_equal(r.outputs["C"].cpu().numpy(), ref["sums"]["C"])
+    if M == 4:
+        assert st[2] > 0 and not r.truncated.any() and np.isnan(r.outputs["Q"].cpu().numpy()).all()
+    else:
+        assert near(r.outputs["Q"].cpu().numpy(), ref["sums"]["Q"])
