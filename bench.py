@@ -2,11 +2,13 @@
 """Benchmark of the tallymap B200 backend on BASELINE config 2: the 1-D random walk, N = 4,194,304 items per GPU.
 
 One STEP = the forward outputs plus the reverse-mode gradient (w.r.t. the broadcast `drift`, cotangent ones on the
-hist tally) over the step's items: "Mitems/s fwd & grad".  The step is timed as ONE fused value-and-grad launch
-(the replay whose count pass is the forward, what value_and_grad runs) where the item has one, else (--unfused, or
-items without one) as a forward launch then the replay launch, whose threads claim items longest first by the
-forward's trip counts (a device argsort inside the step); the separate forward and gradient times are reported too
-(fwd_ms, grad_ms).  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
+hist tally) over the step's items: "Mitems/s fwd & grad".  The step is timed as the ONE value-and-grad launch that
+value_and_grad runs where the item has one: for an item with no active carry (the walkers) the one-pass program,
+which sums each step's VJP as the forward runs (the gradient within the float tolerance of the reverse program's;
+--exact-order times the fused replay instead, bitwise the reverse program's summation order), else the fused
+replay whose count pass is the forward; otherwise (--unfused, or items without one) a forward launch then the
+replay launch, whose threads claim items longest first by the forward's trip counts (a device argsort inside the
+step); the separate forward and gradient (replay) times are reported too (fwd_ms, grad_ms).  Inputs (x0 ~ U(0,1) from PRNGKey(1)'s first subkey, per-item keys split from the
 second) are synthetic, made with jax.random's algorithm on the host (tallymap_b200.prng).  Weak scaling: each rank
 runs its own 4,194,304 items (a contiguous slice of the global item set) and the partial tallies are combined with
 one NCCL collective step (all_reduce of the f32 / i32 tallies, all_gather + on-device combine of the exact gradient
@@ -269,6 +271,9 @@ def main():
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--unfused", action="store_true", help="time the step as a forward and a replay launch")
+    ap.add_argument("--exact-order", action="store_true",
+                    help="time the fused replay (the reverse program's summation order, bitwise) instead of the "
+                         "one-pass value-and-grad of an item with no active carry")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -328,11 +333,15 @@ def main():
                                    go[gnames.index("stats")])
         return out
 
-    # the fused value-and-grad launch (what value_and_grad runs for cotangents given up front), when the item has one
-    fused = None if (tree or args.unfused) else tm.FAMILIES[FAM[cfg.name]].fused.get((0,) if len(cfg.bc) == 1
-                                                                                       else tuple(range(len(cfg.bc))))
-    if fused is not None and not B.pipelined(fused, cfg.max_steps, dev):
-        fused = None                  # (as value_and_grad: the fused replay would be slower than two launches)
+    # the value-and-grad launch value_and_grad runs for cotangents given up front, when the item has one: the one-pass
+    # program for an item with no active carry (unless --exact-order), else the pipelined fused replay
+    wkey = (0,) if len(cfg.bc) == 1 else tuple(range(len(cfg.bc)))
+    fam_ = tm.FAMILIES[FAM[cfg.name]]
+    fused = None if (tree or args.unfused) else (None if args.exact_order else fam_.onepass.get(wkey))
+    if fused is None and not (tree or args.unfused):
+        fused = fam_.fused.get(wkey)
+        if fused is not None and not B.pipelined(fused, cfg.max_steps, dev):
+            fused = None              # (as value_and_grad: the fused replay would be slower than two launches)
     vo = None if fused is None else B.alloc_results(fused, N, dev, max_steps=cfg.max_steps)
     vnames = None if fused is None else [n for n, _, _, _ in fused.result_layout(N)[0]]
 
@@ -448,7 +457,10 @@ def main():
     torch.cuda.synchronize()
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
     dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
-    if fused is not None:
+    if fused is not None and not fused.replay_state_bytes:
+        # the one-pass launch: each forward step (cfg.tf threefry2x32) and its step VJP (cfg.tf_vjp) once
+        dom = (fused.kernel, (cfg.tf + cfg.tf_vjp) * steps_total, v_ms)
+    elif fused is not None:
         # the fused launch: the replay's schedule, its count pass being the forward (cfg.tf threefry2x32 per
         # evaluation), plus the step VJPs
         C_vg = B.replay_plan(fused, cfg.max_steps, None, dev)[0]
@@ -482,8 +494,9 @@ def main():
                    "max_steps": cfg.max_steps, "rev_checkpoints": C_used,
                    "parallelism": f"items sharded over {world} GPU(s)",
                    "l2": "flushed between timed steps (256 MiB write)"},
-        "step": ("one fused value-and-grad launch (" + fused.kernel + ")") if fused is not None else
-                "a forward launch, then the gradient launch(es)",
+        "step": ("one value-and-grad launch (" + fused.kernel + (": the one-pass program, step VJPs summed as the "
+                 "forward runs" if not fused.replay_state_bytes else ": the replay whose count pass is the forward")
+                 + ")") if fused is not None else "a forward launch, then the gradient launch(es)",
         "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3), "separate_ms": round(sep_ms, 3),
         "fused_ms": round(v_ms, 3) if fused is not None else None,
         "fwd_mitems_s": round(N * world / (f_ms / 1e3) / 1e6, 3),

@@ -44,6 +44,20 @@ void team_run(const P& prog, i64 n, int nthreads) {
 // Returns K, the number of steps the forward ran; *final receives the loop's output state.
 template <class P, class S, class A, class Post>
 i64 checkpointed_while(const P& prog, const S& init, int C, A& adj, S* final, Post&& post) {
+  if (C < 0) {
+    // C = -1: the one-pass order of an item with no active carry (each step's VJP applied before the step, oldest
+    // first; post last): the checker of the backend's one-pass value-and-grad programs, not the reference's order
+    S c = init;
+    i64 K = 0;
+    while (prog.cond(c)) {
+      prog.vjp_step(c, adj);
+      c = prog.step(c);
+      ++K;
+    }
+    *final = c;
+    post(c, adj);
+    return K;
+  }
   std::vector<S> head(C + 1), ck(C), tape(C);
   S c = init;
   i64 K = 0;

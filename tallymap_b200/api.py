@@ -99,11 +99,15 @@ class Family:
     in_axes: tuple
     default_max_steps: int
     fused: dict = dataclasses.field(default_factory=dict)   # the same keys -> value-and-grad program (one launch)
+    onepass: dict = dataclasses.field(default_factory=dict)  # the same keys -> one-pass value-and-grad (no active
+                                                              # carry: step VJPs summed as the forward runs)
 
 
 FAMILIES = {
-    "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100, {(0,): B.Q1_VG}),
-    "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000, {(0,): B.RW_VG}),
+    "quickstart": Family("quickstart", B.Q1_FWD, {(0,): B.Q1_GRAD}, (0, 0, None), 100, {(0,): B.Q1_VG},
+                         {(0,): B.Q1_VG1}),
+    "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000, {(0,): B.RW_VG},
+                     {(0,): B.RW_VG1}),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
@@ -171,15 +175,18 @@ class Mapped:
         outs = _poison(tallies, _limits(p, stats))
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
-    def value_and_grad(self, *args, wrt, cotangents, fused=True):
+    def value_and_grad(self, *args, wrt, cotangents, fused=True, exact_order=False):
         """(Result, gradient of <cotangents, outputs>) with the inputs moved to the device once.  The cotangents are
-        given up front, so where the item has a fused program this is ONE launch: the replay's count pass is the
-        forward pass, emitting the forward's tallies while it stores the states the step VJPs then read (bitwise the
-        separate forward and replay; tests/test_fused_gpu.py).  Otherwise (or fused=False) one forward and one
-        replay launch; the replay claims items longest first by the forward's trip counts (an LPT schedule: the
-        replay of an item costs a known function of its trip count), which balances the threads' work and keeps a
-        warp's lanes in the same replay phase; it changes no result (the cotangent tally is exact, per-item results
-        are indexed by item)."""
+        given up front, so where the item has a fused program this is ONE launch.  An item with no active carry (its
+        loop state does not depend on `wrt`: the walkers) runs the one-pass program: each step's VJP is summed as the
+        forward runs, oldest step first, so the gradient equals the reverse program's within the float tolerance
+        (not bitwise: f32 summation order).  With exact_order=True, or for other items, the fused program is the
+        replay whose count pass is the forward pass, emitting the forward's tallies while it stores the states the
+        step VJPs then read (bitwise the separate forward and replay; tests/test_fused_gpu.py).  Otherwise (or
+        fused=False) one forward and one replay launch; the replay claims items longest first by the forward's trip
+        counts (an LPT schedule: the replay of an item costs a known function of its trip count), which balances the
+        threads' work and keeps a warp's lanes in the same replay phase; it changes no result (the cotangent tally is
+        exact, per-item results are indexed by item)."""
         dev = torch.device("cuda", torch.cuda.current_device())
         moved = []
         for a, ax in zip(args, self.fam.in_axes):
@@ -189,7 +196,7 @@ class Mapped:
             else:
                 moved.append(a)
         if fused:
-            r = self._fused(moved, wrt, cotangents)
+            r = self._fused(moved, wrt, cotangents, onepass=not exact_order)
             if r is not None:
                 return r
         res = self(*moved)
@@ -233,18 +240,22 @@ class Mapped:
         return [torch.zeros(t.dims(n), dtype=t.dtype) if cotangents.get(t.name) is None else cotangents[t.name]
                 for t in self.fam.fwd.tallies]
 
-    def _fused(self, args, wrt, cotangents):
-        """(Result, gradient) from the family's value-and-grad program, or None when it has none for `wrt`"""
+    def _fused(self, args, wrt, cotangents, onepass=True):
+        """(Result, gradient) from the family's one-pass (when `onepass`) or fused value-and-grad program, or None
+        when it has none for `wrt`"""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
         if any(self.fam.in_axes[w] is not None for w in idx):
             return None
         bpos = tuple(sum(1 for ax in self.fam.in_axes[:w] if ax is None) for w in idx)
         prog, sel = None, None
-        for key, g in self.fam.fused.items():
-            if all(b in key for b in bpos):
-                prog, sel = g, [key.index(b) for b in bpos]
+        for progs in ((self.fam.onepass,) if onepass else ()) + (self.fam.fused,):
+            for key, g in progs.items():
+                if all(b in key for b in bpos):
+                    prog, sel = g, [key.index(b) for b in bpos]
+                    break
+            if prog is not None:
                 break
-        if prog is None or not B.pipelined(prog, self.max_steps):
+        if prog is None or (prog.replay_state_bytes and not B.pipelined(prog, self.max_steps)):
             return None
         pi, bc = self._split(args)
         n = int(pi[0].shape[0]) if pi else 0

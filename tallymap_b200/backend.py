@@ -198,6 +198,13 @@ Q1_VG = ItemProgram("q1_vg", "q1_vg", pi=Q1_GRAD.pi, bc=Q1_GRAD.bc, consts=Q1_GR
 RW_VG = ItemProgram("rw_vg", "rw_vg", pi=RW_GRAD.pi, bc=RW_GRAD.bc, consts=RW_GRAD.consts,
                     tallies=RW_FWD.tallies + RW_GRAD.tallies, ys=RW_FWD.ys, trunc=1, replay_state_bytes=4,
                     vg_fallback="rw_vg_replay")
+# the one-pass value and grad (OnePassVG: items with no active carry sum each step's VJP as the forward runs; the
+# per-item cotangent is summed oldest step first, so the gradient equals the reverse program's within the float
+# tolerance, not bitwise): the fused layouts without the replay scratch
+Q1_VG1 = ItemProgram("q1_vg_onepass", "q1_vg_onepass", pi=Q1_GRAD.pi, bc=Q1_GRAD.bc, consts=("max_steps",),
+                     tallies=Q1_FWD.tallies + Q1_GRAD.tallies, ys=Q1_FWD.ys, trunc=1)
+RW_VG1 = ItemProgram("rw_vg_onepass", "rw_vg_onepass", pi=RW_GRAD.pi, bc=RW_GRAD.bc, consts=("max_steps",),
+                     tallies=RW_FWD.tallies + RW_GRAD.tallies, ys=RW_FWD.ys, trunc=1)
 
 # BASELINE config 3, the photon slab (csrc/items_photon.cuh)
 PH_FWD = ItemProgram("ph_fwd", "ph_fwd", pi=(KEY,), bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32)),
@@ -241,7 +248,7 @@ SH_GRAD = ItemProgram("sh_grad", "sh_grad", pi=SH_PI,
                       consts=("max_steps", "rev_checkpoints", "replay_threads", "roots", "record"),
                       tallies=(TSpec("ct_X0", (1,), exact=True),), ys=(), replay_state_bytes=4, buffers=18)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, RW_FWD, RW_GRAD, RW_VG, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD,
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, Q1_VG1, RW_FWD, RW_GRAD, RW_VG, RW_VG1, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD,
                                 SH_FWD, SH_REC, SH_GRAD)}
 
 

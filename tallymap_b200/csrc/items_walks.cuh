@@ -333,4 +333,23 @@ struct RWVGMap {
 };
 typedef FusedVG<RWFwd, RWGrad, RWVGMap> RWVG;
 
+// The one-pass value-and-grad programs (OnePassVG, tm_runtime.cuh): the walkers have no active carry, so each step's
+// VJP is summed as the forward runs.  The fused layouts above without the replay scratch; consts = max_steps only.
+//   q1_vg_onepass   x0, keys, theta, ct_hist, consts, order | hist, g_theta, exact, ctl, stats | k, trunc
+//   rw_vg_onepass   x0, keys, drift, ct_hist, ct_side, consts, order | hist, side, g_drift, exact, ctl, stats | k,
+//                   trunc
+struct Q1VG1Map {
+  enum { kNF = Q1Fwd::kNBuf, kNG = Q1Grad::kNBuf, kNBuf = 13 };
+  __host__ __device__ static constexpr int f(int i) { return Q1VGMap::f(i); }
+  __host__ __device__ static constexpr int g(int i) { return i == Q1Grad::kReplay ? 0 : Q1VGMap::g(i); }
+};
+typedef OnePassVG<Q1Fwd, Q1Grad, Q1VG1Map> Q1VG1;
+
+struct RWVG1Map {
+  enum { kNF = RWFwd::kNBuf, kNG = RWGrad::kNBuf, kNBuf = 15 };
+  __host__ __device__ static constexpr int f(int i) { return RWVGMap::f(i); }
+  __host__ __device__ static constexpr int g(int i) { return i == RWGrad::kReplay ? 0 : RWVGMap::g(i); }
+};
+typedef OnePassVG<RWFwd, RWGrad, RWVG1Map> RWVG1;
+
 }  // namespace tmb

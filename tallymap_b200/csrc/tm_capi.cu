@@ -121,6 +121,8 @@ void init_registry() {
   add_vg<tmb::RWVG, 4>("rw_vg");
   add_replay<tmb::Q1VG, 4>("q1_vg_replay");
   add_replay<tmb::RWVG, 4>("rw_vg_replay");
+  add_forward<tmb::Q1VG1>("q1_vg_onepass");
+  add_forward<tmb::RWVG1>("rw_vg_onepass");
   add_forward<tmb::PHFwd>("ph_fwd");
   add_replay<tmb::PHGrad, 1>("ph_grad");
   add_forward<tmb::ODFwd>("od_fwd");

@@ -510,4 +510,73 @@ struct FusedVG {
   }
 };
 
+// An item whose loop carries do not depend on the differentiated operands (no active carry: the walkers, whose
+// operand enters only the emitted values) has a separable adjoint: the VJP of step k needs the state the step starts
+// from and the output cotangents, never a later state or a carry cotangent.  OnePassVG<F, G, Map> sums those step
+// VJPs while the forward runs, for forward_body: no replay, no stored states, one pass over each item.  The
+// gradient is the reverse program's up to the f32 summation order of each item's cotangent (oldest step first here,
+// newest first in the replay: _reverse.py:324-444), within the float tolerance, not bitwise; the per-item sums go
+// into the same exact tally.  F and G as for FusedVG (G's replay scratch, if it has one, is not used: Map::g of
+// G::kReplay may be any index); F::State and G::State are one type; G::adj_finish gets the final state for the
+// initial one (the walkers' pre-loop code has no VJP).
+template <class F, class G, class Map>
+struct OnePassVG {
+  static constexpr int kGSmem = (G::kSmemBytes + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kGSmem + F::kSmemBytes;
+  enum { kConsts = Map::g(G::kConsts), kOrder = Map::g(G::kOrder), kCtl = Map::g(G::kCtl), kNBuf = Map::kNBuf };
+  struct State {
+    typename G::State s;
+    typename G::Adj a;
+  };
+  struct Ctx {
+    typename G::Ctx g;
+    typename F::Ctx f;
+  };
+  __device__ __forceinline__ static Params remap_g(const Params& P) {
+    Params Q;
+#pragma unroll
+    for (int i = 0; i < Map::kNG; ++i) Q.p[i] = P.p[Map::g(i)];
+    return Q;
+  }
+  __device__ __forceinline__ static Params remap_f(const Params& P) {
+    Params Q;
+#pragma unroll
+    for (int i = 0; i < Map::kNF; ++i) Q.p[i] = P.p[Map::f(i)];
+    return Q;
+  }
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    G::setup(c.g, remap_g(P), smem);
+    F::setup(c.f, remap_f(P), smem + kGSmem);
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    G::stage(remap_g(P), smem);
+    F::stage(remap_f(P), smem + kGSmem);
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    State st;
+    st.s = F::start(c.f, item);
+    G::start(c.g, item);
+    G::adj_start(c.g, st.a);
+    return st;
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& st) { return F::cond(c.f, st.s); }
+  __device__ __forceinline__ static void step(const Ctx& c, State& st) {
+    G::vjp(c.g, st.s, st.a);           // the step's VJP at the state it starts from
+    F::step(c.f, st.s);
+  }
+  __device__ static void finish(const Ctx& c, State& st, i64 item) {
+    F::finish(c.f, st.s, item);
+    G::post_vjp(c.g, st.s, st.a);
+    G::adj_finish(c.g, st.s, st.s, st.a, item);
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    G::adj_flush(c.g, const_cast<unsigned char*>(smem), tid, nth);
+    F::flush(c.f, smem + kGSmem, tid, nth);
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int nth) {
+    G::epilogue(c.g, tid, nth);
+    F::epilogue(c.f, tid, nth);
+  }
+};
+
 }  // namespace tmb

@@ -78,10 +78,15 @@ def test_api_value_and_grad_fused_matches_two_launches(cuda):
     x, k = rw_inputs(n, seed=9)
     f = tm.vmap("walk1d", outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None))
     cts = {"hist": torch.ones(256), "side": torch.zeros(2)}
-    r1, g1 = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents=cts)
+    r1, g1 = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents=cts, exact_order=True)
+    assert B.run.last["kernel"] == "rw_vg"
     r2, g2 = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents=cts, fused=False)
+    r3, g3 = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents=cts)      # the one-pass default
+    assert B.run.last["kernel"] == "rw_vg_onepass"
     torch.cuda.synchronize()
     assert np.array_equal(bits(g1.cpu().numpy()), bits(g2.cpu().numpy()))
+    assert near(g3.cpu().numpy(), g2.cpu().numpy())
+    assert np.array_equal(r3.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
     assert np.array_equal(r1.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
     assert np.array_equal(r1.truncated.cpu().numpy(), r2.truncated.cpu().numpy())
     assert near(r1.outputs["hist"].cpu().numpy(), r2.outputs["hist"].cpu().numpy())
@@ -99,3 +104,57 @@ def test_rw_vg_full_size(cuda, orc):
     assert np.array_equal(kk, out[3].cpu().numpy()) and np.array_equal(tr, out[4].cpu().numpy())
     assert np.array_equal(bits(g), bits(gout[0].cpu().numpy()))
     assert near(hist, out[0].cpu().numpy()) and near(side, out[1].cpu().numpy())
+
+
+# ---------------------------------------------------------------------------------------------- one pass
+# The walkers have no active carry: the one-pass programs sum each step's VJP as the forward runs (OnePassVG).  The
+# per-item cotangent is summed oldest step first: bitwise the oracle run in that order (C = -1), within the float
+# tolerance of the reference's newest-first order.
+@pytest.mark.parametrize("n", [1, 777, 20000])
+def test_rw_vg_onepass(cuda, orc, n):
+    x, k = rw_inputs(n, seed=4)
+    ct_h = np.random.default_rng(n).normal(size=256).astype(np.float32)
+    ct_s = np.float32([0.5, -2.0])
+    hist, side, g, stats, kk, tr = vg(B.RW_VG1, [x, k], [np.float32(1.0), ct_h, ct_s], 20000)
+    rf = orc.rw_fwd(x, k, 1.0)
+    assert np.array_equal(kk, rf["k"]) and np.array_equal(tr.astype(bool), rf["trunc"])
+    assert near(hist, rf["hist"]) and near(side, rf["side"])
+    r1 = orc.rw_grad(x, k, 1.0, ct_h, C=-1)
+    assert np.array_equal(bits(g), bits(r1["g"]))
+    rg = orc.rw_grad(x, k, 1.0, ct_h)
+    assert near(g, rg["g"])
+    assert np.array_equal(stats, rf["stats"] + rg["stats"])
+
+
+@pytest.mark.parametrize("ct", ["ones", "random"])
+def test_q1_vg_onepass(cuda, orc, ct):
+    x = np.linspace(0.1, 0.99, 10000, dtype=np.float32)
+    k = prng.split(prng.PRNGKey(0), 10000)
+    c = np.ones(16, np.float32) if ct == "ones" else np.random.default_rng(5).normal(size=16).astype(np.float32)
+    hist, g, stats, kk, tr = vg(B.Q1_VG1, [x, k], [np.float32(2.0), c], 100)
+    rf = orc.q1_fwd(x, k, 2.0)
+    assert np.array_equal(kk, rf["k"]) and np.array_equal(tr.astype(bool), rf["trunc"])
+    assert near(hist, rf["hist"])
+    assert np.array_equal(bits(g), bits(orc.q1_grad(x, k, 2.0, c, C=-1)["g"]))
+    assert near(g, orc.q1_grad(x, k, 2.0, c)["g"])
+
+
+def test_q1_vg_onepass_truncation_poisons(cuda):
+    x = np.linspace(0.1, 0.99, 3000, dtype=np.float32)
+    k = prng.split(prng.PRNGKey(0), 3000)
+    f = tm.vmap("quickstart", outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=3)
+    r, g = f.value_and_grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.ones(16)})
+    assert B.run.last["kernel"] == "q1_vg_onepass"
+    assert int(r.stats["n_truncated"]) > 0 and torch.isnan(g).all() and torch.isnan(r.outputs["hist"]).all()
+
+
+def test_rw_vg_onepass_full_size(cuda, orc):
+    """N = 4,194,304: the one-pass gradient within the float tolerance of the replay's; trip counts bitwise"""
+    x, k = rw_inputs(4194304)
+    ct_h = np.ones(256, np.float32)
+    hist, side, g, stats, kk, tr = vg(B.RW_VG1, [x, k], [np.float32(1.0), ct_h, np.zeros(2, np.float32)], 20000)
+    gout = B.run(B.RW_GRAD, [x, k], [np.float32(1.0), ct_h, np.zeros(2, np.float32)], consts=(20000,))
+    out = B.run(B.RW_FWD, [x, k], [np.float32(1.0)], consts=(20000,))
+    torch.cuda.synchronize()
+    assert np.array_equal(kk, out[3].cpu().numpy()) and np.array_equal(tr, out[4].cpu().numpy())
+    assert near(g, gout[0].cpu().numpy()) and near(hist, out[0].cpu().numpy())

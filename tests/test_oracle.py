@@ -156,3 +156,18 @@ def test_oracle_sh_grad_energy(orc):
     # linearity in the cotangent
     g3 = orc.sh_grad(*inp, ct_dep=2 * ct)
     assert np.allclose(g3["g_E"], 2 * g2["g_E"], rtol=1e-6, atol=1e-6)
+
+
+def test_onepass_order_within_tolerance(orc):
+    """the oracle's one-pass summation order (C = -1, the checker of the one-pass kernels) against the reference's
+    newest-first order: within the float tolerance, and bitwise when every contribution is exact"""
+    from tallymap_b200 import prng
+    kx, ks = prng.split(prng.PRNGKey(3), 2)
+    x, k = prng.uniform(kx, 300), prng.split(ks, 300)
+    ct = np.random.default_rng(1).normal(size=256).astype(np.float32)
+    a, b = orc.rw_grad(x, k, 1.0, ct, C=-1)["g"], orc.rw_grad(x, k, 1.0, ct)["g"]
+    assert abs(float(a[0]) - float(b[0])) <= 1e-5 * abs(float(b[0]))
+    xq = np.linspace(0.1, 0.99, 200, dtype=np.float32)
+    kq = prng.split(prng.PRNGKey(0), 200)
+    a, b = orc.q1_grad(xq, kq, 2.0, np.ones(16, np.float32), C=-1)["g"], orc.q1_grad(xq, kq, 2.0, np.ones(16, np.float32))["g"]
+    assert abs(float(a[0]) - float(b[0])) <= 1e-5 * abs(float(b[0]))
