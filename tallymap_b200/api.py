@@ -467,12 +467,46 @@ class MappedFn:
         _, dts = self.jvp(*args, wrt=idx, tangents=np.eye(len(idx), dtype=np.float32))
         return dts
 
-    def value_and_grad(self, *args, wrt, cotangents):
-        """(Result, gradient): the forward launch and the generated replay launch"""
+    def value_and_grad(self, *args, wrt, cotangents, exact_order=False):
+        """(Result, gradient).  An item whose loop carries do not depend on `wrt` runs ONE generated one-pass launch
+        (each step's VJP summed as the forward runs, oldest step first: the gradient within the float tolerance of
+        the replay's); otherwise, or with exact_order=True, the forward launch and the generated replay launch."""
         dev = torch.device("cuda", torch.cuda.current_device())
         moved = [(a if isinstance(a, torch.Tensor) else torch.from_numpy(B._host(a))).to(dev, non_blocking=True)
                  if ax == 0 else a for a, ax in zip(args, self.in_axes)]
+        if not exact_order:
+            L = self.lowered(moved)
+            idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+            if all(self.in_axes[w] is None for w in idx):
+                bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
+                prog = L.vg_program(bpos)
+                if prog is not None:
+                    return self._onepass(L, prog, moved, wrt, cotangents)
         return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
+
+    def _onepass(self, L, prog, args, wrt, cotangents):
+        pi, bc = self._split(args)
+        cts = []
+        for name, o in self.outputs.items():
+            if o[0] == "records" or o[1] != "f32":
+                continue
+            c = cotangents.get(name)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,))
+        nt = len(L.fwd.tallies)
+        tallies = {t.name: v for t, v in zip(L.fwd.tallies, out[:nt])}
+        ct = out[nt].reshape(-1)
+        stats_raw = out[nt + 1]
+        ys = out[nt + 2:]
+        trunc = ys[prog.trunc].bool()
+        per = list(ys[:L.n_results])
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        bad = _limits(prog, stats)
+        res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        ct = torch.where(bad, torch.full_like(ct, float("nan")), ct)
+        return res, (ct.reshape(()) if isinstance(wrt, int) else ct)
 
 
 def vmap(item, outputs, in_axes, max_steps=None, spawn=None):

@@ -255,7 +255,7 @@ struct ODGrad : OdeCommon {
     i32* stats;
     uint8_t* trunc;
     V3 y_init;
-    mutable ExactPriv<1> pv;
+    mutable ExactPrivS<1> pv;
   };
   typedef OdeState State;
   struct Adj {
@@ -266,7 +266,7 @@ struct ODGrad : OdeCommon {
     float tt, h;
     V3 y, k1;
   };
-  __device__ static void setup(Ctx& c, const Params& P_, unsigned char*) {
+  __device__ static void setup(Ctx& c, const Params& P_, unsigned char* smem) {
     c.sigma = static_cast<const float*>(P_.p[kSigma]);
     c.rho = static_cast<const float*>(P_.p[kRho]);
     c.y0 = static_cast<const float*>(P_.p[kY0]);
@@ -280,7 +280,7 @@ struct ODGrad : OdeCommon {
     c.g = static_cast<float*>(P_.p[kG]);
     c.stats = static_cast<i32*>(P_.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P_.p[kTrunc]);
-    c.pv.zero();
+    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
   }
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static State start(Ctx& c, i64 item) {

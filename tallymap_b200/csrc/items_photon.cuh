@@ -180,7 +180,7 @@ struct PHGrad : PhotonCommon {
     i32* stats;
     uint8_t* trunc;
     Key key;
-    mutable ExactPriv<2> pv;
+    mutable ExactPrivS<2> pv;
   };
   typedef PhotonState State;
   struct Adj {
@@ -189,7 +189,7 @@ struct PHGrad : PhotonCommon {
   struct Stored {
     float px, py, pz, dx, dy, dz, w;
   };
-  __device__ static void setup(Ctx& c, const Params& P, unsigned char*) {
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
     c.keys = static_cast<const uint2*>(P.p[kKeys]);
     c.mu_a = __ldg(static_cast<const float*>(P.p[kMuA]));
     c.mu_s = __ldg(static_cast<const float*>(P.p[kMuS]));
@@ -202,7 +202,7 @@ struct PHGrad : PhotonCommon {
     c.g = static_cast<float*>(P.p[kG]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
-    c.pv.zero();
+    c.pv.bind(smem + ExactBins<2>::kPrivOffset);
   }
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static State start(Ctx& c, i64 item) {

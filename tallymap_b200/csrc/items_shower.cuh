@@ -334,7 +334,7 @@ struct SHGrad {
     Key key;           // the current item's key, energy and newest child
     float E;
     i32 last;
-    mutable ExactPriv<1> pv;
+    mutable ExactPrivS<1> pv;
   };
   struct Adj {
     float ctE, ctd, ctX;
@@ -359,7 +359,7 @@ struct SHGrad {
     c.g = static_cast<float*>(P.p[kGX0]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.tree = static_cast<u32*>(P.p[kTree]);
-    c.pv.zero();
+    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCtDep]);

@@ -105,7 +105,7 @@ struct Q1Grad : Q1Common {
     i32* stats;
     uint8_t* trunc;
     Key key;
-    mutable ExactPriv<1> pv;
+    mutable ExactPrivS<1> pv;
   };
   typedef WalkState State;
   struct Adj {
@@ -120,7 +120,7 @@ struct Q1Grad : Q1Common {
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
     c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
-    c.pv.zero();
+    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCt]);
@@ -243,7 +243,7 @@ struct RWGrad : RWCommon {
     i32* stats;
     uint8_t* trunc;
     Key key;
-    mutable ExactPriv<1> pv;
+    mutable ExactPrivS<1> pv;
   };
   typedef WalkState State;
   struct Adj {
@@ -258,7 +258,7 @@ struct RWGrad : RWCommon {
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
     c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
-    c.pv.zero();
+    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCtHist]);

@@ -142,6 +142,42 @@ __device__ __forceinline__ bool exact_add_word(u64* a, int j, i64 q) {
 // and each thread adds its words into the block's shared words once, when it runs out of items.  Integer addition
 // is associative, so where a value is added first does not change the total: the readout is bitwise the same as
 // adding every emit straight into the global bin.
+// Word j0 of bin b of a thread's private words += q (non-atomic), carries rippling upward: word(b, j) gives word j of
+// bin b (an i64 lvalue).  True if a carry leaves the top word.
+template <class Word>
+__device__ __forceinline__ bool exact_priv_add(Word&& word, int b, int j0, i64 q) {
+#pragma unroll
+  for (int jj = 0; jj < kExactWords; ++jj) {
+    if (jj < j0 || q == 0) continue;
+    i64& w = word(b, jj);
+    const i64 o = w;
+    const i64 r = (i64)((u64)o + (u64)q);
+    w = r;
+    q = (q > 0 && r < o) ? 2 : ((q < 0 && r > o) ? -2 : 0);
+    j0 = jj + 1;
+  }
+  return q != 0;
+}
+
+// The carry-save add of one f32 into bin b of a thread's private words; flag: the bins' flag bits.  Returns true
+// when the bin must be flagged (non-finite, or a carry lost).
+template <class Word>
+__device__ __forceinline__ bool exact_priv_emit(Word&& word, u32& flag, int b, float v) {
+  const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
+  if (e == 255u) { flag |= 1u << b; return true; }
+  const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
+  if (m == 0ull) return false;
+  const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
+  const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
+  const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
+  const bool neg = (bits >> 31) != 0u;
+  bool lost = false;
+  if (lo) lost = exact_priv_add(word, b, (int)j, neg ? -lo : lo);
+  if (hi) lost = exact_priv_add(word, b, (int)j + 1, neg ? -hi : hi) || lost;
+  if (lost) flag |= 1u << b;
+  return lost;
+}
+
 template <int NB>
 struct ExactPriv {
   i64 w[NB][kExactWords];
@@ -154,36 +190,13 @@ struct ExactPriv {
       for (int j = 0; j < kExactWords; ++j) w[b][j] = 0;
     flag = 0u;
   }
-  // word j of bin b += q (non-atomic), carries rippling upward; true if a carry leaves the top word
+  __device__ __forceinline__ i64 word(int b, int j) const { return w[b][j]; }
   __device__ __forceinline__ bool add_word(int b, int j, i64 q) {
-    bool lost = false;
-#pragma unroll
-    for (int jj = 0; jj < kExactWords; ++jj) {
-      if (jj < j || q == 0) continue;
-      const i64 o = w[b][jj];
-      const i64 r = (i64)((u64)o + (u64)q);
-      w[b][jj] = r;
-      q = (q > 0 && r < o) ? 2 : ((q < 0 && r > o) ? -2 : 0);
-      j = jj + 1;
-    }
-    if (q != 0) lost = true;
-    return lost;
+    return exact_priv_add([this](int bb, int jj) -> i64& { return w[bb][jj]; }, b, j, q);
   }
   // add one f32 into bin b; returns true when the bin must be flagged (non-finite, or carry lost)
   __device__ __forceinline__ bool emit(int b, float v) {
-    const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
-    if (e == 255u) { flag |= 1u << b; return true; }
-    const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
-    if (m == 0ull) return false;
-    const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
-    const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
-    const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
-    const bool neg = (bits >> 31) != 0u;
-    bool lost = false;
-    if (lo) lost = add_word(b, (int)j, neg ? -lo : lo);
-    if (hi) lost = add_word(b, (int)j + 1, neg ? -hi : hi) || lost;
-    if (lost) flag |= 1u << b;
-    return lost;
+    return exact_priv_emit([this](int bb, int jj) -> i64& { return w[bb][jj]; }, flag, b, v);
   }
 };
 

@@ -564,10 +564,14 @@ struct OnePassVG {
     G::vjp(c.g, st.s, st.a);           // the step's VJP at the state it starts from
     F::step(c.f, st.s);
   }
-  __device__ static void finish(const Ctx& c, State& st, i64 item) {
-    F::finish(c.f, st.s, item);
-    G::post_vjp(c.g, st.s, st.a);
-    G::adj_finish(c.g, st.s, st.s, st.a, item);
+  // (copies: the loop's state never has its address taken by a call the compiler may not inline, so it stays in
+  // registers for the whole loop)
+  __device__ __forceinline__ static void finish(const Ctx& c, const State& st, i64 item) {
+    const typename G::State s = st.s;
+    typename G::Adj a = st.a;
+    F::finish(c.f, s, item);
+    G::post_vjp(c.g, s, a);
+    G::adj_finish(c.g, s, s, a, item);
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
     G::adj_flush(c.g, const_cast<unsigned char*>(smem), tid, nth);

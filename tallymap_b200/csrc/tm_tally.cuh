@@ -4,19 +4,30 @@
 
 namespace tmb {
 
-// An exact cotangent tally of NB bins: per-thread register words (ExactPriv), merged into the block's shared words
-// when the thread runs out of items, then by one thread into the launch's global words; the last block reads them
-// out (backends/kernel/kernel.py:625-628: a flagged or overflowing bin is NaN, counted in stats[3]).
-// Shared layout: NB x 5 u64 words, then a u32 flag per bin.  Global layout: the same, flags packed after the words.
+// An exact cotangent tally of NB bins: per-thread private words (ExactPrivS: the thread's own slots in shared
+// memory), merged into the block's shared words when the thread runs out of items, then by one thread into the
+// launch's global words; the last block reads them out (backends/kernel/kernel.py:625-628: a flagged or overflowing
+// bin is NaN, counted in stats[3]).
+// Shared layout: NB x 5 u64 words, then a u32 flag per bin (rounded up to 8 bytes), then the private region
+// (kPrivOffset): word (b, j) of thread t at u64 index (b * 5 + j) * TM_BLOCK + t.  Global layout: the words, flags
+// packed after them.
 template <int NB>
 struct ExactBins {
-  static constexpr int kSmemBytes = NB * kExactWords * 8 + ((NB * 4 + 7) / 8) * 8;
-  __device__ static void flush(ExactPriv<NB>& pv, unsigned char* smem, u64* gw, i32* stats, int tid) {
+  static constexpr int kPrivOffset = NB * kExactWords * 8 + ((NB * 4 + 7) / 8) * 8;
+  static constexpr int kSmemBytes = kPrivOffset + NB * kExactWords * 8 * TM_BLOCK;
+  template <class Priv>
+  __device__ static void flush(Priv& pv, unsigned char* smem, u64* gw, i32* stats, int tid) {
     u64* const sw = reinterpret_cast<u64*>(smem);
     u32* const sf = reinterpret_cast<u32*>(smem + NB * kExactWords * 8);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      if (exact_merge_bin(sw + b * kExactWords, pv.w[b])) {
+      bool lost = false;
+#pragma unroll
+      for (int j = 0; j < kExactWords; ++j) {
+        const i64 v = pv.word(b, j);
+        if (v) lost = exact_add_word(sw + b * kExactWords, j, v) || lost;
+      }
+      if (lost) {
         atomicAdd(&stats[kStFixedPointOverflow], 1);
         pv.flag |= 1u << b;
       }
@@ -42,6 +53,24 @@ struct ExactBins {
       if (bad && !gf[b]) atomicAdd(&stats[kStFixedPointOverflow], 1);
       out[b] = (gf[b] || bad) ? __int_as_float(0x7fc00000) : o;
     }
+  }
+};
+
+// A thread-private exact accumulator of NB bins whose words live in the thread's slots of ExactBins<NB>'s private
+// region in shared memory (bind: the region's address), touched once per item.  Held in registers, its 5 words
+// per bin would stay live across the whole step loop and push the step's own values out to local memory.
+template <int NB>
+struct ExactPrivS {
+  i64* w;       // this thread's word (0, 0)
+  u32 flag;     // bit b: bin b saw a non-finite emit or lost a carry
+  __device__ __forceinline__ void bind(unsigned char* region) {
+    w = reinterpret_cast<i64*>(region) + threadIdx.x;
+    flag = 0u;
+  }
+  __device__ __forceinline__ i64& at(int b, int j) const { return w[(b * kExactWords + j) * TM_BLOCK]; }
+  __device__ __forceinline__ i64 word(int b, int j) const { return at(b, j); }
+  __device__ __forceinline__ bool emit(int b, float v) {
+    return exact_priv_emit([this](int bb, int jj) -> i64& { return at(bb, jj); }, flag, b, v);
   }
 };
 

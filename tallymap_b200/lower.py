@@ -277,8 +277,9 @@ def _ref(x, names):
 
 
 # ------------------------------------------------------------------------------------------------ forward program
-def forward_source(it):
-    """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes, tally layout)"""
+def forward_source(it, standalone=True):
+    """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes); standalone=False: the
+    ITEM struct alone (for a combined program)"""
     tr = it.tr
     npi, nbc = len(it.pi), len(it.bc)
     sp = it.spawns
@@ -504,6 +505,8 @@ def forward_source(it):
             lines.append(f"    ExactSum<{S}>::readout(c.x{t}, c.g{t}, c.stats, tid, nth);")
     lines.append("  }")
     lines.append("};")
+    if not standalone:
+        return "\n".join(lines[2:]), max(smem, 16)
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
     lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenFwd>(P, n);")
@@ -673,8 +676,9 @@ class _Rev:
             raise LowerError(f"tallymap_b200.lower: no reverse rule for {p}")
 
 
-def grad_source(it, wrt):
-    """-> (C source of the replay ITEM for d <ct, outputs> / d bc[wrt], shared-memory bytes, stored-state bytes)"""
+def grad_source(it, wrt, standalone=True):
+    """-> (C source of the replay ITEM for d <ct, outputs> / d bc[wrt], stored-state bytes, shared-memory bytes);
+    standalone=False: the ITEM struct alone, its State the forward ITEM's (GenFwd: for the one-pass program)"""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
     act, carry_act = _active(it, wrt)
@@ -712,7 +716,8 @@ def grad_source(it, wrt):
             ctx_ct.append(f"    const float* ct{q};")
             ct_tally[name] = (f"c.ct{q}", S, None)
     lines.append(f"  static constexpr int kSmemBytes = {smem} + {off};")
-    smem_bytes = W * 5 * 8 + ((W * 4 + 7) // 8) * 8 + off       # (ExactBins<W>::kSmemBytes + the staged cotangents)
+    # (ExactBins<W>::kSmemBytes -- block words, flags, the threads' private words -- and the staged cotangents)
+    smem_bytes = W * 5 * 8 + ((W * 4 + 7) // 8) * 8 + W * 5 * 8 * 128 + off
     ctx = ["  struct Ctx {"]
     for j, s in enumerate(it.in_specs[:npi]):
         ctx.append(f"    const {_in_ctype(s)}* in{j};")
@@ -722,14 +727,17 @@ def grad_source(it, wrt):
     ctx += ctx_ct
     for i in it.saved:
         ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
-    ctx.append(f"    mutable ExactPriv<{W}> pv;")
+    ctx.append(f"    mutable ExactPrivS<{W}> pv;")
     ctx.append("  };")
     lines += ctx
-    lines.append("  struct State {")
-    lines.append("    i32 kc;")
-    for j, v in enumerate(tr.carry):
-        lines.append(f"    {CTYPE[v.dtype]} c{j};")
-    lines.append("  };")
+    if standalone:
+        lines.append("  struct State {")
+        lines.append("    i32 kc;")
+        for j, v in enumerate(tr.carry):
+            lines.append(f"    {CTYPE[v.dtype]} c{j};")
+        lines.append("  };")
+    else:
+        lines.append("  typedef GenFwd::State State;")
     stored = [j for j in range(len(tr.carry)) if j not in it.counter]
     lines.append("  struct Stored {")
     for j in stored:
@@ -765,7 +773,7 @@ def grad_source(it, wrt):
             lines.append(f"    c.ct{q} = reinterpret_cast<const float*>(smem + ExactBins<{W}>::kSmemBytes + {o});")
         else:
             lines.append(f"    c.ct{q} = static_cast<const float*>(P.p[kCt{q}]);")
-    lines.append("    c.pv.zero();")
+    lines.append(f"    c.pv.bind(smem + ExactBins<{W}>::kPrivOffset);")
     lines.append("  }")
     lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
     lines += stage_lines
@@ -885,12 +893,65 @@ def grad_source(it, wrt):
     lines.append(f"    if (tid == 0) ExactBins<{W}>::readout(c.gw, c.g, c.stats);")
     lines.append("  }")
     lines.append("};")
+    if not standalone:
+        return "\n".join(lines[2:]), stored_bytes, smem_bytes
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
     lines.append("  tmb::replay_body<tmb::GenGrad, 1>(P, n);")
     lines.append("}")
     lines.append(f"static_assert(tmb::GenGrad::kSmemBytes == {smem_bytes}, \"shared-memory size\");")
     return "\n".join(lines), stored_bytes, smem_bytes
+
+
+# ------------------------------------------------------------------------------------------------ one-pass value and grad
+def has_active_carry(it, wrt):
+    """whether a loop carry depends on the differentiated broadcast operands (else the adjoint is separable: the
+    one-pass program applies)"""
+    return any(_active(it, wrt)[1])
+
+
+def onepass_source(it, wrt):
+    """-> (C source of the one-pass value-and-grad program: the forward and reverse ITEMs combined by OnePassVG for
+    forward_body, shared-memory bytes).  For an item with no active carry: each step's VJP is evaluated at the state
+    the step starts from and summed, oldest step first, as the forward runs.
+    Layout: [per-item][broadcast][output cotangents][consts][order] | [tallies][ct f32[W]][exact words of the
+    fixed-point tallies][ct's exact words][ctl][stats] | [per-item results][truncated]."""
+    tr = it.tr
+    P, Bn = len(it.pi), len(it.bc)
+    Q = sum(1 for _, (_, dt) in it.specs if dt == T.F32)
+    Tn = len(it.specs)
+    X = sum(1 for name, _ in it.specs if name in it.exact)
+    R = len(tr.results)
+    R0 = P + Bn + Q + 2
+    f_map = list(range(P + Bn)) + [P + Bn + Q, P + Bn + Q + 1] + [R0 + t for t in range(Tn)] + \
+        [R0 + Tn + 1 + x for x in range(X)] + [R0 + Tn + 2 + X, R0 + Tn + 3 + X] + \
+        [R0 + Tn + 4 + X + r for r in range(R)] + [R0 + Tn + 4 + X + R]
+    g_map = list(range(P + Bn + Q)) + [P + Bn + Q, P + Bn + Q + 1, R0 + Tn, R0 + Tn + 1 + X, R0 + Tn + 2 + X,
+                                       R0 + Tn + 3 + X, R0 + Tn + 4 + X + R, 0]
+    nbuf = R0 + Tn + 5 + X + R
+    fsrc, fsmem = forward_source(it, standalone=False)
+    gsrc, _, gsmem = grad_source(it, wrt, standalone=False)
+    smem = (gsmem + 15) // 16 * 16 + fsmem
+    lines = [PRELUDE, "namespace tmb {", fsrc, gsrc,
+             "struct GenVGMap {",
+             f"  enum {{ kNF = {len(f_map)}, kNG = {len(g_map)}, kNBuf = {nbuf} }};",
+             "  __host__ __device__ static constexpr int f(int i) {",
+             f"    constexpr int m[kNF] = {{{', '.join(map(str, f_map))}}};",
+             "    return m[i];",
+             "  }",
+             "  __host__ __device__ static constexpr int g(int i) {",
+             f"    constexpr int m[kNG] = {{{', '.join(map(str, g_map))}}};",
+             "    return m[i];",
+             "  }",
+             "};",
+             "typedef OnePassVG<GenFwd, GenGrad, GenVGMap> GenVG;",
+             "static_assert(GenFwd::kNBuf == GenVGMap::kNF && GenGrad::kNBuf == GenVGMap::kNG, \"buffer maps\");",
+             "}  // namespace tmb",
+             'extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {',
+             "  tmb::forward_body<tmb::GenVG>(P, n);",
+             "}",
+             f"static_assert(tmb::GenVG::kSmemBytes == {smem}, \"shared-memory size\");"]
+    return "\n".join(lines), smem, nbuf
 
 
 # ------------------------------------------------------------------------------------------------ programs
@@ -938,6 +999,7 @@ class Lowered:
         self.n_results = len(self.tr.results)
         self.grads = {}
         self.jvps = {}
+        self.vgs = {}
 
     def jvp_program(self, wrt, lanes):
         """the forward-mode program: the forward's outputs and, per tangent lane, the tangents of its float tallies
@@ -963,6 +1025,25 @@ class Lowered:
             self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc, consts=("max_steps",),
                                          tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
         return self.jvps[key]
+
+    def vg_program(self, wrt):
+        """the one-pass value-and-grad program for bc[wrt] (forward outputs, then the exact cotangent tally), or None
+        when a loop carry is active (the adjoint then needs the replay)"""
+        from .backend import ItemProgram, TSpec, Operand
+        wrt = tuple(wrt)
+        if wrt not in self.vgs:
+            prog = None
+            if not (self.fwd.records or self.it.spawns) and not has_active_carry(self.it, list(wrt)):
+                self.grad_program(wrt)            # (the same checks)
+                src, smem, nbuf = onepass_source(self.it, list(wrt))
+                fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
+                bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
+                kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
+                prog = ItemProgram(f"{self.name}_vg", kid, pi=self.pi, bc=bc, consts=("max_steps",),
+                                   tallies=self.fwd.tallies + (TSpec("ct", (len(wrt),), exact=True),),
+                                   ys=self.fwd.ys, trunc=self.fwd.trunc)
+            self.vgs[wrt] = prog
+        return self.vgs[wrt]
 
     def grad_program(self, wrt):
         """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands)"""

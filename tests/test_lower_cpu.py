@@ -196,3 +196,26 @@ def test_ir_evaluator_shower_matches_the_oracle(orc):
     assert np.array_equal(r["results"][0], ref["k"]) and np.array_equal(r["trunc"], ref["trunc"])
     assert int(r["stats"][0]) == int(ref["stats"][0]) and int(r["stats"][4]) == int(ref["stats"][4])
     assert np.abs(r["sums"]["dep"] - ref["dep"]).max() <= 1e-5 * np.abs(ref["dep"]).max()
+
+
+def test_onepass_program_for_items_without_active_carry():
+    """the walk's carries do not depend on drift: a one-pass value-and-grad program (OnePassVG over the generated
+    forward and reverse ITEMs) compiles; the mixer's carries depend on a and b: none"""
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    L = f.lowered(_args_walk())
+    p = L.vg_program((0,))
+    assert p is not None and [t.name for t in p.tallies] == ["hist", "side", "ct"] and p.tallies[-1].exact
+    names = [n for n, _, _, _ in p.result_layout(16)[0]]
+    assert names == ["hist", "side", "ct", "ct.exact", "ctl", "stats", "y0", "truncated"]
+    src = lower.onepass_source(L.it, [0])[0]
+    assert "OnePassVG<GenFwd, GenGrad, GenVGMap>" in src and "typedef GenFwd::State State;" in src
+    kx = prng.split(prng.PRNGKey(3), 8)
+    fm = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), tm.api.torch.int32),
+                                 "end": tm.Sum(())},
+                 in_axes=(0, 0, 0, None, None), max_steps=64)
+    Lm = fm.lowered((np.zeros((8, 3), np.float32), kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
+    assert lower.has_active_carry(Lm.it, [0, 1]) and Lm.vg_program((0, 1)) is None
+    fq = tm.vmap(quickstart, outputs={"hist": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None), max_steps=100)
+    Lq = fq.lowered((np.linspace(0.1, 0.9, 8, dtype=np.float32), prng.split(prng.PRNGKey(0), 8), np.float32(2.0)))
+    pq = Lq.vg_program((0,))
+    assert [n for n, _, _, _ in pq.result_layout(8)[0]][:4] == ["hist", "ct", "hist.exact", "ct.exact"]

@@ -396,3 +396,49 @@ def test_lowered_post_loop_spawn_matches_evaluator(cuda, M):
         assert st[2] > 0 and not r.truncated.any() and np.isnan(r.outputs["Q"].cpu().numpy()).all()
     else:
         assert near(r.outputs["Q"].cpu().numpy(), ref["sums"]["Q"])
+
+
+# ---------------------------------------------------------------------------------------------- one-pass
+def test_lowered_walk_value_and_grad_onepass(cuda, orc):
+    """the traced walk has no active carry: value_and_grad is ONE generated one-pass launch; its gradient is bitwise
+    the oracle summing each item's cotangent oldest step first, within the float tolerance of the replay's order"""
+    x, k = rw_inputs(30000, seed=6)
+    ct = np.random.default_rng(7).normal(size=256).astype(np.float32)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    r, g = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents={"hist": ct})
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    assert B.run.last["kernel"] == f.last_lowered.vg_program((0,)).kernel
+    rf = orc.rw_fwd(x, k, 1.0)
+    assert np.array_equal(r.per_item.cpu().numpy(), rf["k"]) and near(np_out(r)["hist"], rf["hist"])
+    assert np.array_equal(bits(g.cpu().numpy()), bits(orc.rw_grad(x, k, 1.0, ct, C=-1)["g"][0]))
+    g2 = f.value_and_grad(x, k, np.float32(1.0), wrt=2, cotangents={"hist": ct}, exact_order=True)[1]
+    assert np.array_equal(bits(g2.cpu().numpy()), bits(orc.rw_grad(x, k, 1.0, ct)["g"][0]))
+    assert near(g.cpu().numpy(), g2.cpu().numpy())
+
+
+def test_lowered_quickstart_onepass_fixed_point(cuda, orc):
+    """a fixed-point output in the one-pass program: bitwise the forward's exact tally; the gradient bitwise the
+    oracle in the one-pass order"""
+    x = np.linspace(0.1, 0.99, 10000, dtype=np.float32)
+    k = prng.split(prng.PRNGKey(0), 10000)
+    f = tm.vmap(quickstart, outputs={"hist": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None), max_steps=100)
+    r, g = f.value_and_grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.ones(16)})
+    r0 = f(x, k, np.float32(2.0))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(np_out(r)["hist"]), bits(np_out(r0)["hist"]))
+    assert np.array_equal(bits(g.cpu().numpy()), bits(orc.q1_grad(x, k, 2.0, np.ones(16, np.float32), C=-1)["g"][0]))
+
+
+def test_lowered_mixer_value_and_grad_uses_replay(cuda):
+    """the mixer's carries depend on a and b: value_and_grad is the forward and the replay"""
+    kx = prng.split(prng.PRNGKey(3), 512)
+    rng = np.random.default_rng(2)
+    pos = rng.uniform(-1, 1, (512, 3)).astype(np.float32)
+    n = rng.integers(1, 40, 512).astype(np.int32)
+    f = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), torch.int32), "end": tm.Sum(())},
+                in_axes=(0, 0, 0, None, None), max_steps=64)
+    r, g = f.value_and_grad(pos, kx, n, np.float32(0.3), np.float32(1.7), wrt=(3, 4),
+                            cotangents={"end": torch.ones(())})
+    assert B.run.last["kernel"] == f.last_lowered.grad_program((0, 1)).kernel
+    assert torch.isfinite(g).all()
