@@ -46,10 +46,21 @@ enum { kStSpawned = 0, kStChildrenDropped = 1, kStChildrenTruncated = 2, kStFixe
 // (kernel.py:137-150; bitwise jax.random's threefry2x32_p).  A rotate is one funnel shift.
 __device__ __forceinline__ u32 rotl(u32 x, int d) { return __funnelshift_l(x, x, d); }
 
+// A round is an add, a rotate and an xor: three instructions of the integer ALU pipe, which bounds threefry.  Each
+// round's add is written as a multiply-add by 1 held in constant memory (a value the compiler cannot fold), so it
+// issues on the multiply-add pipe instead, beside the ALU's rotate and xor: at full occupancy on a B200 that ran
+// threefry2x32 at 445 G/s against 389 G/s with plain adds, the results bitwise the same (x * 1 + y == x + y mod 2^32).
+static __constant__ u32 kTmOne = 1u;
+__device__ __forceinline__ u32 add_mad(u32 a, u32 b) {
+  u32 d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(b), "r"(kTmOne), "r"(a));
+  return d;
+}
+
 __device__ __forceinline__ void threefry2x32(u32 k0, u32 k1, u32 c0, u32 c1, u32& o0, u32& o1) {
   const u32 k2 = k0 ^ k1 ^ 0x1BD11BDAu;
   u32 x0 = c0 + k0, x1 = c1 + k1;
-#define TM_R(r) x0 += x1; x1 = rotl(x1, r); x1 ^= x0;
+#define TM_R(r) x0 = add_mad(x0, x1); x1 = rotl(x1, r); x1 ^= x0;
   TM_R(13) TM_R(15) TM_R(26) TM_R(6)  x0 += k1; x1 += k2 + 1u;
   TM_R(17) TM_R(29) TM_R(16) TM_R(24) x0 += k2; x1 += k0 + 2u;
   TM_R(13) TM_R(15) TM_R(26) TM_R(6)  x0 += k0; x1 += k1 + 3u;
