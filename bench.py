@@ -459,8 +459,8 @@ def main():
     peak = used.value * iters / (pe[0].elapsed_time(pe[1]) / 1e3) / 1e9
     dom = (cfg.grad.kernel, tf_grad, g_ms) if g_ms >= f_ms else (cfg.fwd.kernel, tf_fwd, f_ms)
     if fused is not None and not fused.replay_state_bytes:
-        # the one-pass launch: each forward step (cfg.tf threefry2x32) and its step VJP (cfg.tf_vjp) once
-        dom = (fused.kernel, (cfg.tf + cfg.tf_vjp) * steps_total, v_ms)
+        # the one-pass launch: each forward step once (cfg.tf threefry2x32); its gradient part draws nothing
+        dom = (fused.kernel, cfg.tf * steps_total, v_ms)
     elif fused is not None:
         # the fused launch: the replay's schedule, its count pass being the forward (cfg.tf threefry2x32 per
         # evaluation), plus the step VJPs
@@ -476,7 +476,8 @@ def main():
                 f"ncu dram bytes read+write of one launch at N={tr[1]}, scaled by items to N={N}",
                 "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
                 "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
-                "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, {cfg.tf_vjp} per step VJP; "
+                "work": f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
+                        f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
                         "steps from the per-item trip counts and the replay schedule)"} if cfg.tf else None
 
     cpu = None

@@ -334,12 +334,38 @@ struct PhGrad : PhBase<MathT> {
     a.ct_frac = a.ct_frac + cv * w;
     a.ct_w = ct_w + cv * this->frac;
   }
+  // C = -1: forward mode, the order of the backend's one-pass program (the tangent tw of w w.r.t. albedo carried
+  // with the state; each deposit adds cv * w to ct_frac and (cv * frac) * tw to ct_albedo): the checker of that
+  // program, not the reference's order
+  void forward_mode(PhState& s, Adj& a) const {
+    float tw = 0.0f;
+    while (cond(s)) {
+      const Key nk = fold_in(kk, (u32)s.k);
+      const float u0 = uniform_f32(nk, 0u, 0.0f, 1.0f), u3 = uniform_f32(nk, 3u, 0.0f, 1.0f);
+      const float sl = this->path(u0);
+      const float px = s.px + sl * s.dx, py = s.py + sl * s.dy, pz = s.pz + sl * s.dz;
+      const bool inside = this->in_box(px) && this->in_box(py) && this->in_box(pz);
+      const i32 flat = (this->voxel(px) * 64 + this->voxel(py)) * 64 + this->voxel(pz);
+      const float cv = inside ? ct[flat] : 0.0f;
+      a.ct_frac = a.ct_frac + cv * s.w;
+      a.ct_albedo = a.ct_albedo + (cv * this->frac) * tw;
+      const float w1 = s.w * this->albedo, tw1 = tw * this->albedo + s.w;
+      const bool low = w1 < 0.001f, survive = u3 < 0.1f;
+      tw = low ? (survive ? tw1 * 10.0f : 0.0f) : tw1;
+      s = step(s);
+    }
+  }
   void item(i64 i, Priv& p) const {
     PhGrad me = *this;
     me.kk = this->key(i);
     Adj a{0.0f, 0.0f, 0.0f};
     PhState fin;
-    checkpointed_while(me, this->start(), C, a, &fin, [](const PhState&, Adj& ad) { ad.ct_w = 0.0f; });
+    if (C < 0) {
+      fin = this->start();
+      me.forward_mode(fin, a);
+    } else {
+      checkpointed_while(me, this->start(), C, a, &fin, [](const PhState&, Adj& ad) { ad.ct_w = 0.0f; });
+    }
     trunc[i] = (fin.kc >= this->M && fin.alive) ? 1 : 0;
     const float r = 1.0f / (this->mu_t * this->mu_t);
     const float ct_mu_t = ((-a.ct_frac) * this->mu_a) * r + ((-a.ct_albedo) * this->mu_s) * r;

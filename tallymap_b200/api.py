@@ -108,7 +108,7 @@ FAMILIES = {
                          {(0,): B.Q1_VG1}),
     "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000, {(0,): B.RW_VG},
                      {(0,): B.RW_VG1}),
-    "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000),
+    "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000, {}, {(0, 1): B.PH_VG1}),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
     "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000),
@@ -180,7 +180,8 @@ class Mapped:
         given up front, so where the item has a fused program this is ONE launch.  An item with no active carry (its
         loop state does not depend on `wrt`: the walkers) runs the one-pass program: each step's VJP is summed as the
         forward runs, oldest step first, so the gradient equals the reverse program's within the float tolerance
-        (not bitwise: f32 summation order).  With exact_order=True, or for other items, the fused program is the
+        (not bitwise: f32 summation order); the photon's one-pass program is forward mode (its one active carry's
+        tangent travels with the state), again within the float tolerance.  With exact_order=True, or for other items, the fused program is the
         replay whose count pass is the forward pass, emitting the forward's tallies while it stores the states the
         step VJPs then read (bitwise the separate forward and replay; tests/test_fused_gpu.py).  Otherwise (or
         fused=False) one forward and one replay launch; the replay claims items longest first by the forward's trip

@@ -248,7 +248,13 @@ SH_GRAD = ItemProgram("sh_grad", "sh_grad", pi=SH_PI,
                       consts=("max_steps", "rev_checkpoints", "replay_threads", "roots", "record"),
                       tallies=(TSpec("ct_X0", (1,), exact=True),), ys=(), replay_state_bytes=4, buffers=18)
 
-PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, Q1_VG1, RW_FWD, RW_GRAD, RW_VG, RW_VG1, PH_FWD, PH_GRAD, OD_FWD, OD_GRAD,
+# the photon's value and grad in one forward pass by forward mode (w's tangent w.r.t. albedo carried with the state;
+# csrc/items_photon.cuh PHVG1): within the float tolerance of the replay's gradient
+PH_VG1 = ItemProgram("ph_vg_onepass", "ph_vg_onepass", pi=PH_GRAD.pi, bc=PH_GRAD.bc, consts=("max_steps",),
+                     tallies=PH_FWD.tallies + PH_GRAD.tallies, ys=PH_FWD.ys, trunc=1)
+
+PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, Q1_VG1, RW_FWD, RW_GRAD, RW_VG, RW_VG1, PH_FWD, PH_GRAD, PH_VG1,
+                                OD_FWD, OD_GRAD,
                                 SH_FWD, SH_REC, SH_GRAD)}
 
 

@@ -267,4 +267,114 @@ struct PHGrad : PhotonCommon {
   }
 };
 
+// ================================================================================================= one pass
+// Value and gradient in one forward pass, by forward mode: the only active carry is w, and its tangent with respect
+// to albedo travels with the state (tw: w1 = w * albedo gives tw1 = tw * albedo + w; the roulette scales both by the
+// same 10 or 0).  Each deposit w * frac adds cv * w to the cotangent of frac and (cv * frac) * tw to that of albedo
+// (cv = ct_dep at the voxel, 0 outside); at the item's end the pre-loop code's VJP maps (frac, albedo) to (mu_a,
+// mu_s) as in PHGrad::adj_finish.  The same gradient as the replay adjoint, summed in another order (forward, not
+// newest first): within the float tolerance, not bitwise.  No replay scratch: the forward's cost plus a load of
+// ct_dep and four multiply-adds per step.
+//   ph_vg_onepass  keys, mu_a, mu_s, ct_dep f32[64^3], consts i32[1], order | dep f32[64^3], g f32[2],
+//                  dep accumulator f64[64^3], exact u64[11], ctl, stats | k i32[N], trunc u8[N]
+struct PHVG1 : PhotonCommon {
+  enum { kKeys, kMuA, kMuS, kCtDep, kConsts, kOrder, kDep, kG, kDep64, kExact, kCtl, kStats, kK, kTrunc, kNBuf };
+  static constexpr int kW = PHFwd::kW, kW0 = PHFwd::kW0;
+  static constexpr int kXBytes = (ExactBins<2>::kSmemBytes + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kXBytes + PHFwd::kSmemBytes;
+  struct Ctx {
+    const uint2* keys;
+    float mu_a, mu_s, mu_t, albedo, frac;
+    i32 M;
+    const float* ct;
+    float* dep;
+    double* dep64;
+    u64* gw;
+    float* g;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+    Key key;
+    float* win;
+    mutable ExactPrivS<2> pv;
+  };
+  struct State {
+    PhotonState s;
+    float tw, cf, ca;     // d w / d albedo; the item's cotangents of frac and albedo so far
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.win = reinterpret_cast<float*>(smem + kXBytes);
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.mu_a = __ldg(static_cast<const float*>(P.p[kMuA]));
+    c.mu_s = __ldg(static_cast<const float*>(P.p[kMuS]));
+    c.mu_t = c.mu_a + c.mu_s;
+    c.albedo = c.mu_s / c.mu_t;
+    c.frac = c.mu_a / c.mu_t;
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
+    c.ct = static_cast<const float*>(P.p[kCtDep]);
+    c.dep = static_cast<float*>(P.p[kDep]);
+    c.dep64 = static_cast<double*>(P.p[kDep64]);
+    c.gw = static_cast<u64*>(P.p[kExact]);
+    c.g = static_cast<float*>(P.p[kG]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.kout = static_cast<i32*>(P.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.pv.bind(smem + ExactBins<2>::kPrivOffset);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    c.key = Key{kk.x, kk.y};
+    return State{PhotonState{0, 0, 32.0f, 32.0f, 0.0f, 0.0f, 0.0f, 1.0f, 1.0f, true}, 0.0f, 0.0f, 0.0f};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& st) { return st.s.kc < c.M && st.s.alive; }
+  __device__ __forceinline__ static void step(const Ctx& c, State& st) {
+    PhotonState& s = st.s;
+    const Draws u = draws(c.key, s.k);
+    const float sl = path(u.u0, c.mu_t);
+    s.px = s.px + sl * s.dx;
+    s.py = s.py + sl * s.dy;
+    s.pz = s.pz + sl * s.dz;
+    const bool inside = in_box(s.px) && in_box(s.py) && in_box(s.pz);
+    const i32 ix = voxel(s.px), iy = voxel(s.py), iz = voxel(s.pz);
+    const i32 flat = (ix * kBox + iy) * kBox + iz;
+    const bool in_win = (u32)(ix - kW0) < (u32)kW && (u32)(iy - kW0) < (u32)kW && iz < kW;
+    const i32 widx = in_win ? ((ix - kW0) * kW + (iy - kW0)) * kW + iz : -1;
+    datom_warp_window(c.dep64, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
+    const float cv = inside ? __ldg(&c.ct[flat]) : 0.0f;
+    st.cf = st.cf + cv * s.w;
+    st.ca = st.ca + (cv * c.frac) * st.tw;
+    const float w1 = s.w * c.albedo, tw1 = st.tw * c.albedo + s.w;
+    scatter(s, u.u1, u.u2);
+    const bool low = w1 < 0.001f, survive = u.u3 < 0.1f;
+    s.w = low ? (survive ? w1 * 10.0f : 0.0f) : w1;
+    st.tw = low ? (survive ? tw1 * 10.0f : 0.0f) : tw1;
+    s.alive = inside && !(low && !survive);
+    s.kc += 1;
+    s.k += 1;
+  }
+  __device__ static void finish(const Ctx& c, const State& st, i64 item) {
+    c.kout[item] = st.s.k;
+    c.trunc[item] = (st.s.kc >= c.M && st.s.alive) ? 1 : 0;
+    const float r = 1.0f / (c.mu_t * c.mu_t);
+    const float ct_mu_t = ((-st.cf) * c.mu_a) * r + ((-st.ca) * c.mu_s) * r;
+    if (c.pv.emit(0, st.cf / c.mu_t + ct_mu_t)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+    if (c.pv.emit(1, st.ca / c.mu_t + ct_mu_t)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    ExactBins<2>::flush(c.pv, const_cast<unsigned char*>(smem), c.gw, c.stats, tid);
+    const float* win = reinterpret_cast<const float*>(smem + kXBytes);
+    for (int b = tid; b < kW * kW * kW; b += nth) {
+      const float v = win[b];
+      if (v == 0.0f) continue;
+      const int ix = kW0 + b / (kW * kW), iy = kW0 + (b / kW) % kW, iz = b % kW;
+      atomicAdd(&c.dep64[(ix * kBox + iy) * kBox + iz], (double)v);
+    }
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int nth) {
+    if (tid == 0) ExactBins<2>::readout(c.gw, c.g, c.stats);
+    f64_to_f32(c.dep64, c.dep, kS, tid, nth);
+  }
+};
+
 }  // namespace tmb

@@ -125,6 +125,7 @@ void init_registry() {
   add_forward<tmb::RWVG1>("rw_vg_onepass");
   add_forward<tmb::PHFwd>("ph_fwd");
   add_replay<tmb::PHGrad, 1>("ph_grad");
+  add_forward<tmb::PHVG1>("ph_vg_onepass");
   add_forward<tmb::ODFwd>("od_fwd");
   add_replay<tmb::ODGrad, 1>("od_grad");
   add_spawn<tmb::SHFwd>("sh_fwd");

@@ -115,3 +115,56 @@ def test_ph_full_size_properties(cuda):
     gb = gpu_ph_grad(keys)
     assert np.array_equal(ga["g"].view(np.uint32), gb["g"].view(np.uint32))
     assert np.isfinite(ga["g"]).all() and ga["g"][0] > 0
+
+
+# ---------------------------------------------------------------------------------------------- one pass
+def gpu_ph_vg1(keys, mu_a=0.1, mu_s=10.0, ct=None, M=100000):
+    ct = np.ones((64, 64, 64), np.float32) if ct is None else ct
+    out = B.run(B.PH_VG1, [keys], [np.float32(mu_a), np.float32(mu_s), ct], consts=(M,))
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    dep, g, stats, k, tr = [o.cpu().numpy() for o in out]
+    return dict(dep=dep, g=g, stats=stats, k=k, trunc=tr.astype(bool))
+
+
+@pytest.mark.parametrize("n", [1, 20000])
+def test_ph_vg_onepass(cuda, orc, n):
+    """forward mode in one pass: the forward's outputs as the forward's; the gradient bitwise the oracle's forward
+    mode (C = -1) and within the float tolerance of the replay adjoint's"""
+    keys = prng.split(prng.PRNGKey(2), n)
+    ct = np.random.default_rng(4).uniform(0.5, 1.5, (64, 64, 64)).astype(np.float32)
+    got = gpu_ph_vg1(keys, ct=ct)
+    ref = orc.ph_fwd(keys)
+    assert np.array_equal(got["k"], ref["k"]) and np.array_equal(got["trunc"], ref["trunc"])
+    assert near(got["dep"], ref["dep"])
+    fm = orc.ph_grad(keys, ct=ct, C=-1)
+    assert np.array_equal(got["g"].view(np.uint32), fm["g"].view(np.uint32))
+    rv = orc.ph_grad(keys, ct=ct)
+    assert near(got["g"], rv["g"])
+    assert np.array_equal(got["stats"], ref["stats"] + rv["stats"])
+
+
+def test_ph_vg_onepass_params_and_truncation(cuda, orc):
+    keys = prng.split(prng.PRNGKey(7), 4000)
+    for mu_a, mu_s, M in ((1.0, 2.0, 100000), (0.01, 30.0, 300)):
+        got = gpu_ph_vg1(keys, mu_a, mu_s, M=M)
+        fm = orc.ph_grad(keys, mu_a, mu_s, max_steps=M, C=-1)
+        assert np.array_equal(got["g"].view(np.uint32), fm["g"].view(np.uint32))
+        assert np.array_equal(got["trunc"], fm["trunc"])
+        assert near(got["g"], orc.ph_grad(keys, mu_a, mu_s, max_steps=M)["g"])
+
+
+def test_ph_api_value_and_grad_onepass(cuda):
+    """value_and_grad of the photon family runs the one-pass program; the gradient within the float tolerance of
+    the forward + replay launches (exact_order=True)"""
+    import tallymap_b200 as tm
+    keys = prng.split(prng.PRNGKey(3), 300000)
+    f = tm.vmap("photon", outputs={"dep": tm.Sum((64, 64, 64))}, in_axes=(0, None, None))
+    cts = {"dep": torch.ones((64, 64, 64))}
+    r1, g1 = f.value_and_grad(keys, np.float32(0.1), np.float32(10.0), wrt=(1, 2), cotangents=cts)
+    assert B.run.last["kernel"] == "ph_vg_onepass"
+    r2, g2 = f.value_and_grad(keys, np.float32(0.1), np.float32(10.0), wrt=(1, 2), cotangents=cts, exact_order=True)
+    torch.cuda.synchronize()
+    assert near(g1.cpu().numpy(), g2.cpu().numpy())
+    assert np.array_equal(r1.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
+    assert near(r1.outputs["dep"].cpu().numpy(), r2.outputs["dep"].cpu().numpy())
