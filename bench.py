@@ -115,11 +115,12 @@ def configs(B):
         "od": Cfg("od", B.OD_FWD, B.OD_GRAD, od_inputs, [8.0 / 3.0], ["ones(N,3)", np.float32(1.0)],
                   ["final", "mean_z"], 50000, 0, 0, 1048576,
                   "Lorenz RK45 ensemble (BASELINE config 4): forward + replay grad w.r.t. beta"),
-        # the gradient is the tree adjoint: the recording forward, the generation lists, one adjoint launch per
-        # generation and one over the roots (backend.tree_grad)
+        # the separate gradient is the tree adjoint: the recording forward, the generation lists, one adjoint launch
+        # per generation and one over the roots (backend.tree_grad); the step is the one-pass spawn launch (forward
+        # mode through spawn) unless --exact-order
         "sh": Cfg("sh", B.SH_FWD, B.SH_GRAD, sh_inputs, [1.0], [np.ones(512, np.float32)], ["dep", "count"], 100000,
                   0, 0, 1048576,
-                  "branching shower (BASELINE config 5): forward + tree-adjoint grad w.r.t. X0 (items = roots)"),
+                  "branching shower (BASELINE config 5): forward + grad w.r.t. the roots' E0 and X0 (items = roots)"),
     }
 
 
@@ -343,10 +344,19 @@ def main():
         fused = fam_.fused.get(wkey)
         if fused is not None and not B.pipelined(fused, cfg.max_steps, dev):
             fused = None              # (as value_and_grad: the fused replay would be slower than two launches)
+    # the shower's one spawn launch (forward mode through spawn), what value_and_grad runs for it
+    sh_vg = tree and not (args.unfused or args.exact_order)
+    if sh_vg:
+        fused = B.SH_VG1
     vo = None if fused is None else B.alloc_results(fused, N, dev, max_steps=cfg.max_steps)
     vnames = None if fused is None else [n for n, _, _, _ in fused.result_layout(N)[0]]
 
     def vg():
+        if sh_vg:
+            r = B.sh_value_and_grad(pi, bc[0], ct[0], max_steps=cfg.max_steps, out=vo)
+            if world > 1:
+                parallel.all_reduce_sums([r["dep"], r["count"], r["stats"]])
+            return r
         out = B.run(fused, pi, bc + ct, consts=(cfg.max_steps,), out=vo)
         if world > 1:
             parallel.all_reduce_sums(out[:ntal] + [out[ntal + 1]])
@@ -496,8 +506,9 @@ def main():
                    "max_steps": cfg.max_steps, "rev_checkpoints": C_used,
                    "parallelism": f"items sharded over {world} GPU(s)",
                    "l2": "flushed between timed steps (256 MiB write)"},
-        "step": ("one value-and-grad launch (" + fused.kernel + (": the one-pass program, step VJPs summed as the "
-                 "forward runs" if not fused.replay_state_bytes else ": the replay whose count pass is the forward")
+        "step": ("one value-and-grad launch (" + fused.kernel + (": the one-pass program, the gradient accumulated "
+                 "as the forward runs" if not fused.replay_state_bytes else ": the replay whose count pass is the "
+                 "forward")
                  + ")") if fused is not None else "a forward launch, then the gradient launch(es)",
         "fwd_ms": round(f_ms, 3), "grad_ms": round(g_ms, 3), "separate_ms": round(sep_ms, 3),
         "fused_ms": round(v_ms, 3) if fused is not None else None,
@@ -510,7 +521,8 @@ def main():
            if tree else {}),
         "e2e": {"value": round(e2e_val, 3), "unit": "Mitems/s",
                 "h2d_bytes_per_step": int(sum(h.nbytes for h in host)), "d2h_bytes_per_step": int(d2h[0])},
-        "gpu_launches": args.steps * ((1 + tree_info["kernels"]) if tree else
+        # (the shower's one-pass step: the spawn launch and the per-root readout of the exact words)
+        "gpu_launches": args.steps * ((2 if sh_vg else 1 + tree_info["kernels"]) if tree else
                                       ((1 if fused is not None else 2) + (1 if world > 1 else 0))),
         "roofline": roofline,
         "clocks": clk,

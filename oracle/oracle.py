@@ -73,6 +73,7 @@ def lib():
             L.or_sh_fwd.argtypes = [i64, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
             L.or_od_grad.argtypes = [i64, P, P, P, P, f32, P, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
             L.or_sh_grad.argtypes = [i64, P, P, P, f32, P, i32, ctypes.c_int, P, P, P, P]
+            L.or_sh_vg1.argtypes = [i64, P, P, P, f32, P, i32, ctypes.c_int, P, P]
             _LIB = L
     return _LIB
 
@@ -277,6 +278,18 @@ def sh_fwd(E0, d0, keys, X0=1.0, max_steps=100000, nthreads=0, f64acc=True):
     lib().or_sh_fwd(n, _p(E0), _p(d0), _p(keys), X0, max_steps, nthreads, _p(dep), _p(count), _p(k), _p(tr), _p(st),
                     int(f64acc))
     return dict(dep=dep, count=count, k=k, trunc=tr.astype(bool), stats=st)
+
+
+def sh_vg1(E0, d0, keys, X0=1.0, ct_dep=None, max_steps=100000, nthreads=0):
+    """the one-pass shower gradient (forward mode through spawn, exact per-root sums): g_E[n]"""
+    E0, d0 = np.ascontiguousarray(E0, np.float32), np.ascontiguousarray(d0, np.float32)
+    keys = np.ascontiguousarray(keys, np.uint32)
+    n = len(E0)
+    ct = np.ones(512, np.float32) if ct_dep is None else np.ascontiguousarray(ct_dep, np.float32)
+    gE = np.zeros(n, np.float32)
+    st = np.zeros(5, np.int32)
+    lib().or_sh_vg1(n, _p(E0), _p(d0), _p(keys), X0, _p(ct), max_steps, nthreads, _p(gE), _p(st))
+    return dict(g_E=gE, stats=st)
 
 
 def sh_grad(E0, d0, keys, X0=1.0, ct_dep=None, max_steps=100000, nthreads=0):

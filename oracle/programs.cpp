@@ -902,6 +902,57 @@ int or_od_grad(i64 n, const float* sigma, const float* rho, const float* y0, con
   return 0;
 }
 
+// Forward mode through spawn, the checker of the backend's one-pass shower program (not the reference's order):
+// each particle carries the tangent tE of its energy w.r.t. its root's E0 (a root 1; children tE * z and
+// tE * (1 - z), as their energies E * z and E * (1 - z)); a deposit of E at bin b adds ct[b] * tE (one f32
+// product) to its root's exact sum.  Depth and X0 reach the outputs only through the integer bin index, so their
+// cotangents are zero.
+struct ShVG1 {
+  const float *E0, *d0;
+  const u32* keys;
+  float X0;
+  i32 M;
+  const float* ct;
+  float* gE;
+  i32* stats;
+  struct P { float E, depth, tE; Key key; };
+  struct Priv { std::vector<P> stack; };
+  void item(i64 i, Priv& pv) const {
+    ExactBins acc(1);
+    pv.stack.push_back(P{E0[i], d0[i], 1.0f, Key{keys[2 * i], keys[2 * i + 1]}});
+    while (!pv.stack.empty()) {
+      const P p = pv.stack.back();
+      pv.stack.pop_back();
+      i32 kc = 0, k = 0;
+      bool alive = true;
+      const float E = p.E;
+      float depth = p.depth;
+      while (kc < M && alive) {
+        const Key kk = fold_in(p.key, (u32)k);
+        const float u0 = uniform_f32(kk, 0u, 0.0f, 1.0f), u1 = uniform_f32(kk, 1u, 0.0f, 1.0f);
+        const float u2 = uniform_f32(kk, 2u, 0.0f, 1.0f);
+        depth = depth + X0 * (-tmm::logf(1.0f - u0));
+        const bool low = E < 0.5f;
+        if (low) {
+          const i32 b = f2i_rz(depth * 8.0f);
+          if ((u32)b < 512u) exact_emit_priv(acc, 0, ct[b] * p.tE, stats);
+        }
+        const bool split = !low && u1 < 0.7f;
+        if (split) {
+          const float z = 0.1f + 0.8f * u2;
+          pv.stack.push_back(P{E * (1.0f - z), depth, p.tE * (1.0f - z), fold_in(kk, 1u)});
+          pv.stack.push_back(P{E * z, depth, p.tE * z, fold_in(kk, 0u)});
+        }
+        alive = !low && !split;
+        kc += 1;
+        k += 1;
+      }
+    }
+    exact_readout(acc, 1, &gE[i], stats);
+  }
+  void flush(Priv&) const {}
+};
+
 // the tree adjoint: g_X0 (exact), g_E[n], g_depth[n]; stats[2] counts truncated particles of the whole forest
 int or_sh_grad(i64 n, const float* E0, const float* d0, const u32* keys, float X0, const float* ct_dep, i32 max_steps,
                int nthreads, float* g_X0, float* g_E, float* g_depth, i32* stats) {
@@ -911,6 +962,15 @@ int or_sh_grad(i64 n, const float* E0, const float* d0, const u32* keys, float X
   p.gE = g_E; p.gD = g_depth; p.stats = stats; p.gbins = &gb;
   team_run(p, n, nthreads);
   exact_readout(gb, 1, g_X0, stats);
+  return 0;
+}
+
+// the one-pass (forward mode) gradient of <ct_dep, dep> w.r.t. each root's E0: g_E[n]
+int or_sh_vg1(i64 n, const float* E0, const float* d0, const u32* keys, float X0, const float* ct_dep, i32 max_steps,
+              int nthreads, float* g_E, i32* stats) {
+  ShVG1 p;
+  p.E0 = E0; p.d0 = d0; p.keys = keys; p.X0 = X0; p.M = max_steps; p.ct = ct_dep; p.gE = g_E; p.stats = stats;
+  team_run(p, n, nthreads);
   return 0;
 }
 

@@ -196,6 +196,8 @@ class Mapped:
                 moved.append(t.to(dev, non_blocking=True))
             else:
                 moved.append(a)
+        if fused and "tree" in self.fam.grads and not exact_order:
+            return self._onepass_tree(moved, wrt, cotangents)
         if fused:
             r = self._fused(moved, wrt, cotangents, onepass=not exact_order)
             if r is not None:
@@ -276,6 +278,27 @@ class Mapped:
         res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
         ct = torch.where(bad, torch.full_like(ct, float("nan")), ct)
         return res, (ct.reshape(()) if isinstance(wrt, int) else ct)
+
+    def _onepass_tree(self, args, wrt, cotangents):
+        """(Result, gradient) of the shower in one spawn launch: forward mode through spawn (backend.sh_value_and_grad),
+        the gradient within the float tolerance of the tree adjoint's; NaN when a limit intervened"""
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        pi, bc = self._split(args)
+        c = cotangents.get("dep")
+        ct = torch.zeros(512, dtype=torch.float32) if c is None else c
+        r = B.sh_value_and_grad(pi, bc[0], ct, max_steps=self.max_steps, queue=self.queue)
+        p = self.fam.fwd
+        trunc = r["trunc"].bool()
+        n_tr = trunc.sum(dtype=torch.int32)
+        stats = {nm: r["stats"][i] for i, nm in enumerate(B.STATS)}
+        stats["n_truncated"] = n_tr
+        bad = _limits(p, stats)
+        res = Result(_poison({"dep": r["dep"], "count": r["count"]}, bad), r["k"], trunc, stats)
+        by_arg = {0: r["g_E"], 1: r["g_depth"], 3: r["g_X0"].reshape(())}
+        if any(w not in by_arg for w in idx):
+            raise ValueError(f"tallymap_b200: item {self.fam.name!r} is differentiable in arguments {sorted(by_arg)}")
+        g = tuple(torch.where(bad, torch.full_like(by_arg[w], float("nan")), by_arg[w]) for w in idx)
+        return res, (g[0] if isinstance(wrt, int) else g)
 
     def _tree_grad(self, args, idx, cotangents, wrt):
         """the gradient of a spawning item through its children (tallymap/_reverse_spawn.py:233-336): the recording

@@ -14,6 +14,7 @@ Records layout after a launch).
 
 Everything runs on the GPU through libtm_b200.so; there is no CPU path.  Device memory and streams come from torch.
 """
+import ctypes
 import dataclasses
 from typing import Tuple
 
@@ -238,6 +239,13 @@ SH_FWD = ItemProgram("sh_fwd", "sh_fwd", pi=(Operand("E", (), _F32), Operand("de
 # its reverse mode (the tree adjoint): the recording forward (the forward's outputs plus every child's record and
 # each root's newest child) and the per-generation adjoint, launched by tree_grad
 SH_PI = (Operand("E", (), _F32), Operand("depth", (), _F32), KEY)
+# the shower's value and gradient w.r.t. the roots' E0 in one spawn launch, by forward mode through spawn (each particle
+# carries d E / d E0 of its root; csrc/items_shower.cuh SHVG1): per-root exact sums, read out by sh_value_and_grad
+SH_VG1 = ItemProgram("sh_vg_onepass", "sh_vg_onepass", pi=SH_PI,
+                     bc=(Operand("X0", (), _F32), Operand("ct_dep", (512,), _F32)), consts=("max_steps", "queue", "items"),
+                     tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32), TSpec("g_E", ("N",), exact=True)),
+                     ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1, spawns=True,
+                     queue_leaf_bytes=24)
 SH_REC = ItemProgram("sh_rec", "sh_rec", pi=SH_PI, bc=(Operand("X0", (), _F32),), consts=("max_steps", "queue", "record"),
                      tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32)),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8),
@@ -254,8 +262,7 @@ PH_VG1 = ItemProgram("ph_vg_onepass", "ph_vg_onepass", pi=PH_GRAD.pi, bc=PH_GRAD
                      tallies=PH_FWD.tallies + PH_GRAD.tallies, ys=PH_FWD.ys, trunc=1)
 
 PROGRAMS = {p.name: p for p in (Q1_FWD, Q1_GRAD, Q1_VG, Q1_VG1, RW_FWD, RW_GRAD, RW_VG, RW_VG1, PH_FWD, PH_GRAD, PH_VG1,
-                                OD_FWD, OD_GRAD,
-                                SH_FWD, SH_REC, SH_GRAD)}
+                                OD_FWD, OD_GRAD, SH_FWD, SH_REC, SH_GRAD, SH_VG1)}
 
 
 # -------------------------------------------------------------------------------------------------- run
@@ -402,7 +409,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     replay_bytes = 0
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
     R = record_capacity(N, record, dev) if p.record_bytes else 0
-    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q, "record": R}
+    known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q, "record": R, "items": N}
     if p.replay_state_bytes:
         C, threads, replay_bytes = replay_plan(p, known["max_steps"], rev_checkpoints, dev)
         known.update(rev_checkpoints=C, replay_threads=threads)
@@ -464,6 +471,24 @@ def record_capacity(N, record=None, device=None):
 
 
 TREE_MAX_GEN = 1024     # generations the tree adjoint takes (deeper trees: NaN gradient, counted)
+
+
+def sh_value_and_grad(pi, X0, ct_dep, max_steps=100000, queue=None, stream=None, out=None):
+    """the shower's forward outputs and the gradient of <ct_dep, dep> in ONE spawn launch (forward mode through
+    spawn, SH_VG1), then the per-root readout of the exact words (tm_exact_combine).  d/d depth0 and d/d X0 are
+    zero: depth and X0 reach the outputs only through the integer bin index (the tree adjoint gives the same +0).
+    -> dict(dep, count, stats, k, trunc, g_E, g_depth, g_X0) as device tensors (g_E NaN for a root whose sum
+    overflowed; the caller poisons on truncation and dropped children)"""
+    st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    res = run(SH_VG1, pi, [X0, ct_dep], consts=(max_steps,), queue=queue, stream=st, out=out)
+    dep, count, g_E, stats, k, tr = res
+    N = int(k.shape[0])
+    if N:
+        words = run.last["results"]["g_E.exact"]
+        _lib.check(_lib.lib().tm_exact_combine(ctypes.c_void_p(st), ctypes.c_void_p(words.data_ptr()), 1, N,
+                                               ctypes.c_void_p(g_E.data_ptr()), ctypes.c_void_p(stats.data_ptr())))
+    return dict(dep=dep, count=count, stats=stats, k=k, trunc=tr, g_E=g_E, g_depth=torch.zeros_like(g_E),
+                g_X0=torch.zeros(1, dtype=torch.float32, device=g_E.device))
 
 
 def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):

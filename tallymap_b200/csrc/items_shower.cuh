@@ -144,6 +144,159 @@ struct SHFwd {
   __device__ static void epilogue(const Ctx&, int, int) {}
 };
 
+// ------------------------------------------------------------------------------------ one pass: forward mode
+// The shower's value and gradient in one spawn launch.  Only E reaches an emitted value (the deposit E when low);
+// depth and X0 reach the outputs only through the integer bin index, so their cotangents are zero (the tree adjoint
+// computes the same +0).  E is linear along a particle's ancestry (a child has E * z or E * (1 - z), z independent
+// of E), so each particle carries the tangent tE of its E w.r.t. its root's E0 (a root 1; children tE * z and
+// tE * (1 - z)) and its root's index; a deposit at bin b adds ct_dep[b] * tE (one f32 product) to its root's
+// gradient.  A thread keeps the exact words of its current root in its shared-memory slots (ExactPrivS) and merges
+// them into the root's global exact words (atomics) when it starts a particle of another root and at the end, so
+// each root's gradient is the correctly rounded exact sum of its contributions: the same whatever thread ran which
+// particle.  The same gradient as the tree adjoint, summed differently: within the float tolerance, not bitwise.
+//   sh_vg_onepass  E0, depth0, keys, X0, ct_dep f32[512], consts (max_steps, Q, N), order | dep f32[512], count i32[1],
+//                  g_E f32[N] (read out from the words by the host's exact combine), g_E exact words
+//                  u64[5N + (N + 1) / 2], seq, qctl, ctl, stats | k i32[N], trunc u8[N], ring (E, depth, key, tE,
+//                  root)[Q]
+struct ShowerVGChild {
+  float E, depth;
+  u32 ka, kb;
+  float tE;
+  i32 root;
+};
+
+struct ShowerVGState {
+  i32 kc, k;
+  float E, depth;
+  Key key;
+  bool alive;
+  float tE;
+  i32 root;
+};
+
+struct SHVG1 {
+  enum { kE0, kDepth0, kKeys, kX0, kCtDep, kConsts, kOrder, kDep, kCount, kGOut, kGE, kSeq, kQctl, kCtl, kStats, kK,
+         kTrunc, kQueue, kNBuf };
+  enum { kConstM, kConstQ, kConstN };
+  static constexpr int kNB = 512;
+  static constexpr int kXOff = kNB * 4 + 16;                       // after the dep bins and the count word
+  static constexpr int kCtOff = kXOff + ExactBins<1>::kSmemBytes;  // ct_dep staged
+  static constexpr int kSmemBytes = kCtOff + kNB * 4;
+  typedef ShowerVGChild Child;
+  typedef ShowerVGState State;
+  struct Ctx {
+    const float *E0, *d0;
+    const uint2* keys;
+    float X0;
+    i32 M, N;
+    float* sh;
+    i32* shc;
+    const float* ct;
+    float* dep;
+    i32* count;
+    u64* gE;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+    mutable i32 n;            // particles this thread finished
+    mutable i32 cur;          // the root whose words this thread's slots hold (-1: none)
+    mutable ExactPrivS<1> pv;
+  };
+  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
+    c.E0 = static_cast<const float*>(P.p[kE0]);
+    c.d0 = static_cast<const float*>(P.p[kDepth0]);
+    c.keys = static_cast<const uint2*>(P.p[kKeys]);
+    c.X0 = __ldg(static_cast<const float*>(P.p[kX0]));
+    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]) + kConstM);
+    c.N = __ldg(static_cast<const i32*>(P.p[kConsts]) + kConstN);
+    c.sh = reinterpret_cast<float*>(smem);
+    c.shc = reinterpret_cast<i32*>(smem + kNB * 4);
+    c.ct = reinterpret_cast<const float*>(smem + kCtOff);
+    c.dep = static_cast<float*>(P.p[kDep]);
+    c.count = static_cast<i32*>(P.p[kCount]);
+    c.gE = static_cast<u64*>(P.p[kGE]);
+    c.stats = static_cast<i32*>(P.p[kStats]);
+    c.kout = static_cast<i32*>(P.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.n = 0;
+    c.cur = -1;
+    c.pv.bind(smem + kXOff + ExactBins<1>::kPrivOffset);
+  }
+  __device__ static void stage(const Params& P, unsigned char* smem) {
+    const float* ct = static_cast<const float*>(P.p[kCtDep]);
+    float* d = reinterpret_cast<float*>(smem + kCtOff);
+    for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
+  }
+  // this thread's words of root c.cur into the root's global words (then zeroed); a lost carry or a flagged word
+  // flags the root (NaN at readout)
+  __device__ static void merge(const Ctx& c) {
+    if (c.cur < 0) return;
+    u64* const w = c.gE + (i64)c.cur * kExactWords;
+    bool lost = false;
+#pragma unroll
+    for (int j = 0; j < kExactWords; ++j) {
+      const i64 v = c.pv.word(0, j);
+      if (v) lost = exact_add_word(w, j, v) || lost;
+      c.pv.at(0, j) = 0;
+    }
+    if (lost) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+    if (lost || (c.pv.flag & 1u)) {
+      // flag words after the N roots' words: u32 per root (the exact scratch layout)
+      atomicOr(reinterpret_cast<u32*>(c.gE + (i64)c.N * kExactWords) + c.cur, 1u);
+    }
+    c.pv.flag = 0u;
+  }
+  __device__ static State start(Ctx& c, i64 item) {
+    const uint2 kk = __ldg(&c.keys[item]);
+    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true, 1.0f, (i32)item};
+  }
+  __device__ static State start_child(Ctx&, const Child& ch) {
+    return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true, ch.tE, ch.root};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
+    const ShowerStepOut o = shower_advance(c.X0, s);
+    if (o.low) {
+      const i32 b = f2i(s.depth * 8.0f);
+      SumPriv<kNB>::emit(c.sh, c.stats, b, s.E);
+      if ((u32)b < (u32)kNB) {
+        if (s.root != c.cur) {
+          merge(c);
+          c.cur = s.root;
+        }
+        if (c.pv.emit(0, c.ct[b] * s.tE)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+      }
+    }
+    if (o.split) {
+      const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
+      o0 = Child{s.E * o.z, s.depth, c0.a, c0.b, s.tE * o.z, s.root};
+      o1 = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b, s.tE * (1.0f - o.z), s.root};
+      n_out = 2;
+    }
+  }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {
+    c.n += 1;
+    const bool tr = s.kc >= c.M && s.alive;
+    if (child) {
+      if (tr) atomicAdd(&c.stats[kStChildrenTruncated], 1);
+    } else {
+      c.kout[item] = s.k;
+      c.trunc[item] = tr ? 1 : 0;
+    }
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
+    merge(c);
+    SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.dep, tid, nth);
+    if (c.n) atomicAdd(c.shc, c.n);
+    __syncthreads();
+    if (tid == 0) {
+      const i32 v = *reinterpret_cast<const i32*>(smem + kNB * 4);
+      if (v) atomicAdd(c.count, v);
+    }
+  }
+  __device__ static void epilogue(const Ctx&, int, int) {}
+};
+
 // ------------------------------------------------------------------------------------ reverse mode: the tree adjoint
 // The reference differentiates through spawn with a recording primal and one adjoint launch per generation
 // (tallymap/_reverse_spawn.py:1-45): the record holds every child's initial state, parent, ordinal and generation;

@@ -130,6 +130,7 @@ void init_registry() {
   add_replay<tmb::ODGrad, 1>("od_grad");
   add_spawn<tmb::SHFwd>("sh_fwd");
   add_spawn<tmb::SHRec>("sh_rec");
+  add_spawn<tmb::SHVG1>("sh_vg_onepass");
   add_replay<tmb::SHGrad, 1>("sh_grad");
 }
 

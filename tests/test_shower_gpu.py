@@ -134,3 +134,59 @@ def test_sh_tree_grad_full_size(cuda, orc):
     idx = np.random.default_rng(0).choice(1048576, 64, replace=False)
     ref = orc.sh_grad(inp[0][idx], inp[1][idx], inp[2][idx])
     assert np.array_equal(a["ct_E"][idx].view(np.uint32), ref["g_E"].view(np.uint32))
+
+
+# ---------------------------------------------------------------------------------------------- one pass
+def near_roots(a, b):
+    """per root: within 1e-5 relative, or 1e-6 absolute for near-zero roots (the float tolerance)"""
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return bool(np.all(np.abs(a - b) <= np.maximum(1e-5 * np.abs(b), 1e-6)))
+
+
+@pytest.mark.parametrize("n", [1, 777, 20000])
+def test_sh_vg_onepass(cuda, orc, n):
+    """forward mode through spawn in one launch: the forward's outputs as the forward's; g_E bitwise the oracle's
+    forward mode (exact per-root sums) and within the float tolerance of the tree adjoint's"""
+    inp = orc.sh_inputs(n)
+    ct = np.random.default_rng(n).normal(size=512).astype(np.float32)
+    r = B.sh_value_and_grad(list(inp), np.float32(1.0), ct)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    ref = orc.sh_fwd(*inp)
+    assert np.array_equal(r["count"].cpu().numpy(), ref["count"])
+    assert np.array_equal(r["k"].cpu().numpy(), ref["k"])
+    assert np.array_equal(r["stats"].cpu().numpy(), ref["stats"])
+    assert np.abs(r["dep"].cpu().numpy().astype(np.float64) - ref["dep"]).max() <= FT * np.abs(ref["dep"]).max()
+    gE = r["g_E"].cpu().numpy()
+    assert np.array_equal(gE.view(np.uint32), orc.sh_vg1(*inp, ct_dep=ct)["g_E"].view(np.uint32))
+    tg = orc.sh_grad(*inp, ct_dep=ct)
+    assert near_roots(gE, tg["g_E"])
+    assert not r["g_depth"].any() and not tg["g_depth"].any() and float(tg["g_X0"][0]) == 0.0
+
+
+def test_sh_api_value_and_grad_onepass(cuda):
+    """value_and_grad of the shower runs the one spawn launch; against the recording forward + tree adjoint"""
+    import tallymap_b200 as tm
+    from oracle import oracle as orc
+    inp = orc.sh_inputs(50000)
+    f = tm.vmap("shower", outputs={"dep": tm.Sum((512,)), "count": tm.Sum((1,), torch.int32)},
+                in_axes=(0, 0, 0, None))
+    cts = {"dep": torch.from_numpy(np.random.default_rng(3).normal(size=512).astype(np.float32))}
+    r1, (gE1, gX1) = f.value_and_grad(*inp, np.float32(1.0), wrt=(0, 3), cotangents=cts)
+    assert B.run.last["kernel"] == "sh_vg_onepass"
+    r2, (gE2, gX2) = f.value_and_grad(*inp, np.float32(1.0), wrt=(0, 3), cotangents=cts, exact_order=True)
+    torch.cuda.synchronize()
+    assert near_roots(gE1.cpu().numpy(), gE2.cpu().numpy())
+    assert float(gX1) == 0.0 and float(gX2) == 0.0
+    assert np.array_equal(r1.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
+    assert int(r1.outputs["count"][0]) == int(r2.outputs["count"][0])
+
+
+def test_sh_vg_onepass_small_queue_poisons(cuda, orc):
+    """a queue too small: dropped children poison the gradient (NaN), never a silently partial one"""
+    import tallymap_b200 as tm
+    inp = orc.sh_inputs(5000)
+    f = tm.vmap("shower", outputs={"dep": tm.Sum((512,)), "count": tm.Sum((1,), torch.int32)},
+                in_axes=(0, 0, 0, None), spawn=tm.Queue(64))
+    r, gE = f.value_and_grad(*inp, np.float32(1.0), wrt=0, cotangents={"dep": torch.ones(512)})
+    assert int(r.stats["children_dropped"]) > 0 and torch.isnan(gE).all()
