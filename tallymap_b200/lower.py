@@ -1027,21 +1027,31 @@ class Lowered:
         return self.jvps[key]
 
     def vg_program(self, wrt):
-        """the one-pass value-and-grad program for bc[wrt] (forward outputs, then the exact cotangent tally), or None
-        when a loop carry is active (the adjoint then needs the replay)"""
+        """the one-pass value-and-grad program for bc[wrt] (forward outputs, then the exact cotangent tally): with no
+        active carry the step VJPs summed as the forward runs (OnePassVG); otherwise, for up to FWD_GRAD_MAX
+        operands and no fixed-point output, forward mode with the tangents contracted at each emit
+        (jvp_source(contract=True)); else None (the replay)"""
         from .backend import ItemProgram, TSpec, Operand
         wrt = tuple(wrt)
         if wrt not in self.vgs:
             prog = None
-            if not (self.fwd.records or self.it.spawns) and not has_active_carry(self.it, list(wrt)):
+            if not (self.fwd.records or self.it.spawns):
                 self.grad_program(wrt)            # (the same checks)
-                src, smem, nbuf = onepass_source(self.it, list(wrt))
                 fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
                 bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
-                kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
-                prog = ItemProgram(f"{self.name}_vg", kid, pi=self.pi, bc=bc, consts=("max_steps",),
-                                   tallies=self.fwd.tallies + (TSpec("ct", (len(wrt),), exact=True),),
-                                   ys=self.fwd.ys, trunc=self.fwd.trunc)
+                tallies = self.fwd.tallies + (TSpec("ct", (len(wrt),), exact=True),)
+                if not has_active_carry(self.it, list(wrt)):
+                    src, smem, nbuf = onepass_source(self.it, list(wrt))
+                    kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
+                elif len(wrt) <= FWD_GRAD_MAX and not self.it.exact:
+                    src, smem = jvp_source(self.it, list(wrt), len(wrt), contract=True)
+                    nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 1 + 2 + len(self.fwd.ys)
+                    kid = compile_kernel(src, f"{self.name}_fg{''.join(map(str, wrt))}", nbuf, smem)
+                else:
+                    kid = None
+                if kid is not None:
+                    prog = ItemProgram(f"{self.name}_vg", kid, pi=self.pi, bc=bc, consts=("max_steps",),
+                                       tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
             self.vgs[wrt] = prog
         return self.vgs[wrt]
 
@@ -1075,6 +1085,8 @@ class Lowered:
 
 # ------------------------------------------------------------------------------------------------ forward mode
 LANES_MAX = 16        # tangent lanes of one jvp program (the reference's jacfwd lanes, LANES_MAX_LOCAL)
+FWD_GRAD_MAX = 4      # value_and_grad by forward mode (one lane per operand) for items with an active carry: up to
+                      # this many differentiated operands, else the replay
 
 
 def _jvp_rule(e, a, d, out):
@@ -1158,12 +1170,19 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
     return out
 
 
-def jvp_source(it, wrt, L):
+def jvp_source(it, wrt, L, contract=False):
     """-> (C source of the forward ITEM with L tangent lanes of the broadcast operands bc[wrt], shared-memory bytes).
     Buffers: [per-item][broadcast][tangent seeds f32[L, W]][consts][order] | [tallies][tangent tallies f32[L, S] of
-    the float tallies][ctl][stats] | [per-item results][truncated]"""
+    the float tallies][ctl][stats] | [per-item results][truncated].
+    contract=True: the one-pass value-and-grad by forward mode, for cotangents given up front: L = W lanes seeded
+    with the identity, each tangent emit contracted with the output's cotangent at its index into a per-item sum per
+    lane, the sums emitted once per item into an exact W-bin tally.  Buffers: [per-item][broadcast][output
+    cotangents of the float tallies][consts][order] | [tallies][ct f32[W]][ct's exact words][ctl][stats] |
+    [per-item results][truncated]"""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
+    if contract:
+        L = W
     if not 1 <= L <= LANES_MAX:
         raise LowerError(f"tallymap_b200.lower: 1..{LANES_MAX} tangent lanes")
     act, carry_act = _active(it, wrt)
@@ -1175,13 +1194,21 @@ def jvp_source(it, wrt, L):
         enum.append(f"kIn{j} = {idx}"); idx += 1
     for k in range(nbc):
         enum.append(f"kBc{k} = {idx}"); idx += 1
-    enum.append(f"kTan = {idx}"); idx += 1
+    if contract:
+        for q, _ in enumerate(ftal):
+            enum.append(f"kCt{q} = {idx}"); idx += 1
+    else:
+        enum.append(f"kTan = {idx}"); idx += 1
     enum.append(f"kConsts = {idx}"); idx += 1
     enum.append(f"kOrder = {idx}"); idx += 1
     for t, _ in enumerate(it.specs):
         enum.append(f"kT{t} = {idx}"); idx += 1
-    for q, _ in enumerate(ftal):
-        enum.append(f"kD{q} = {idx}"); idx += 1
+    if contract:
+        enum.append(f"kG = {idx}"); idx += 1
+        enum.append(f"kExact = {idx}"); idx += 1
+    else:
+        for q, _ in enumerate(ftal):
+            enum.append(f"kD{q} = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
@@ -1190,6 +1217,14 @@ def jvp_source(it, wrt, L):
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
     smem, priv = 0, {}
+    if contract:
+        # the exact cotangent bins with the threads' private words first, then the staged output cotangents
+        smem = (W * 5 * 8 + ((W * 4 + 7) // 8) * 8 + W * 5 * 8 * 128 + 15) // 16 * 16
+        for q, (t, name, shape) in enumerate(ftal):
+            S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+            if S * 4 <= PRIV_BYTES:
+                priv[("c", name)] = smem
+                smem += (S * 4 + 15) // 16 * 16
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
         if S * 4 <= PRIV_BYTES:
@@ -1197,7 +1232,7 @@ def jvp_source(it, wrt, L):
             smem += (S * 4 + 15) // 16 * 16
     for q, (t, name, shape) in enumerate(ftal):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
-        if L * S * 4 <= PRIV_BYTES:
+        if not contract and L * S * 4 <= PRIV_BYTES:
             priv[("d", name)] = smem
             smem += (L * S * 4 + 15) // 16 * 16
     lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
@@ -1219,9 +1254,14 @@ def jvp_source(it, wrt, L):
         if ("p", name) in priv:
             ctx.append(f"    {ct}* s{t};")
     for q, (t, name, shape) in enumerate(ftal):
+        if contract:
+            ctx.append(f"    const float* ct{t};")
+            continue
         ctx.append(f"    float* gd{t};")
         if ("d", name) in priv:
             ctx.append(f"    float* sd{t};")
+    if contract:
+        ctx += ["    u64* gw;", "    float* g;", f"    mutable ExactPrivS<{W}> pv;"]
     for r, y in enumerate(tr.results):
         ctx.append(f"    {CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}* y{r};")
     act_saved = [i for i in it.saved if i in act]
@@ -1239,6 +1279,9 @@ def jvp_source(it, wrt, L):
         if carry_act[j]:
             for l in range(L):
                 lines.append(f"    float d{j}_{l};")
+    if contract:
+        for l in range(L):
+            lines.append(f"    float a{l};   // the item's cotangent of bc[{wrt[l]}] so far")
     lines.append("  };")
     tidx = {name: t for t, (name, _) in enumerate(it.specs)}
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -1248,7 +1291,10 @@ def jvp_source(it, wrt, L):
         lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
     for q, k in enumerate(wrt):
         for l in range(L):
-            lines.append(f"    c.db{k}_{l} = __ldg(static_cast<const float*>(P.p[kTan]) + {l * W + q});")
+            if contract:
+                lines.append(f"    c.db{k}_{l} = {'1.0f' if l == q else '0.0f'};")
+            else:
+                lines.append(f"    c.db{k}_{l} = __ldg(static_cast<const float*>(P.p[kTan]) + {l * W + q});")
     lines += ["    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));",
               "    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
     for t, (name, (shape, dt)) in enumerate(it.specs):
@@ -1257,13 +1303,33 @@ def jvp_source(it, wrt, L):
         if ("p", name) in priv:
             lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[('p', name)]});")
     for q, (t, name, shape) in enumerate(ftal):
+        if contract:
+            if ("c", name) in priv:
+                lines.append(f"    c.ct{t} = reinterpret_cast<const float*>(smem + {priv[('c', name)]});")
+            else:
+                lines.append(f"    c.ct{t} = static_cast<const float*>(P.p[kCt{q}]);")
+            continue
         lines.append(f"    c.gd{t} = static_cast<float*>(P.p[kD{q}]);")
         if ("d", name) in priv:
             lines.append(f"    c.sd{t} = reinterpret_cast<float*>(smem + {priv[('d', name)]});")
+    if contract:
+        lines += ["    c.gw = static_cast<u64*>(P.p[kExact]);", "    c.g = static_cast<float*>(P.p[kG]);",
+                  f"    c.pv.bind(smem + ExactBins<{W}>::kPrivOffset);"]
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
     lines.append("  }")
-    lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
+    if contract:
+        lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
+        for q, (t, name, shape) in enumerate(ftal):
+            if ("c", name) in priv:
+                S = int(np.prod(shape, dtype=np.int64)) if shape else 1
+                lines.append(f"    {{ const float* src = static_cast<const float*>(P.p[kCt{q}]); "
+                             f"float* d = reinterpret_cast<float*>(smem + {priv[('c', name)]}); "
+                             f"for (int b = threadIdx.x; b < {S}; b += blockDim.x) d[b] = __ldg(&src[b]); }}")
+        lines.append("  }")
+    else:
+        lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
+    acc = {"p": "a"}
 
     def emitter(name, idx_c, v_c):
         t, S, dt = tidx[name], sizes[name], it.tr.specs[name][1]
@@ -1279,6 +1345,10 @@ def jvp_source(it, wrt, L):
 
     def temitter(name, l, idx_c, dv_c):
         t, S = tidx[name], sizes[name]
+        if contract:
+            # the tangent emit contracted with the cotangent at its index (an out-of-range index adds nothing)
+            a_ = f"{acc['p']}{l}"
+            return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) {a_} = {a_} + c.ct{t}[b_] * {dv_c}; }}"
         tgt = f"c.sd{t}" if ("d", name) in priv else f"c.gd{t}"
         # (an out-of-range index is counted once, by the primal emit)
         return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) fatom(&{tgt}[{l * S} + b_], {dv_c}); }}"
@@ -1288,6 +1358,10 @@ def jvp_source(it, wrt, L):
     lines.append("  __device__ static State start(Ctx& c, i64 item) {")
     names = _names_pre(it)
     tn = dict(bc_t)
+    if contract:
+        acc["p"] = "a"
+        for l in range(L):
+            lines.append(f"    float a{l} = 0.0f;")
     for v, ld in it.loads:
         lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
     lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter)
@@ -1297,6 +1371,9 @@ def jvp_source(it, wrt, L):
         for l in range(L):
             lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
     lines += ["    State s;", "    s.kc = 0;"]
+    if contract:
+        for l in range(L):
+            lines.append(f"    s.a{l} = a{l};")
     for j, x in enumerate(tr.carry_in):
         lines.append(f"    s.c{j} = {_ref(x, names)};")
         if carry_act[j]:
@@ -1320,6 +1397,7 @@ def jvp_source(it, wrt, L):
     lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
     names = _names_loop(it, tr.carry)
     tn = loop_tn(tr.carry, "s")
+    acc["p"] = "s.a"
     lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter)
     for j, x in enumerate(tr.body_out):
         lines.append(f"    const {CTYPE[tr.carry[j].dtype]} n{j} = {_ref(x, names)};")
@@ -1336,12 +1414,21 @@ def jvp_source(it, wrt, L):
     lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
     names = _names_loop(it, tr.post_carry)
     tn = loop_tn(tr.post_carry, "s")
+    if contract:
+        acc["p"] = "a"
+        for l in range(L):
+            lines.append(f"    float a{l} = s.a{l};")
     lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter)
+    if contract:
+        for l in range(L):
+            lines.append(f"    if (c.pv.emit({l}, a{l})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
     lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
     lines.append("  }")
     lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
+    if contract:
+        lines.append(f"    ExactBins<{W}>::flush(c.pv, const_cast<unsigned char*>(smem), c.gw, c.stats, tid);")
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = sizes[name]
         if ("p", name) in priv:
@@ -1353,10 +1440,16 @@ def jvp_source(it, wrt, L):
         if ("d", name) in priv:
             lines.append(f"    SumPriv<{L * sizes[name]}>::flush(c.sd{t}, c.gd{t}, tid, nth);")
     lines.append("  }")
-    lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
+    if contract:
+        lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int) {")
+        lines.append(f"    if (tid == 0) ExactBins<{W}>::readout(c.gw, c.g, c.stats);")
+        lines.append("  }")
+    else:
+        lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
     lines.append("};")
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
     lines.append("  tmb::forward_body<tmb::GenJvp>(P, n);")
     lines.append("}")
+    lines.append(f"static_assert(tmb::GenJvp::kSmemBytes == {max(smem, 16)}, \"shared-memory size\");")
     return "\n".join(lines), max(smem, 16)

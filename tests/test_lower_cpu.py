@@ -200,7 +200,7 @@ def test_ir_evaluator_shower_matches_the_oracle(orc):
 
 def test_onepass_program_for_items_without_active_carry():
     """the walk's carries do not depend on drift: a one-pass value-and-grad program (OnePassVG over the generated
-    forward and reverse ITEMs) compiles; the mixer's carries depend on a and b: none"""
+    forward and reverse ITEMs) compiles; the mixer's carries depend on a and b: forward mode instead"""
     f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
     L = f.lowered(_args_walk())
     p = L.vg_program((0,))
@@ -214,8 +214,24 @@ def test_onepass_program_for_items_without_active_carry():
                                  "end": tm.Sum(())},
                  in_axes=(0, 0, 0, None, None), max_steps=64)
     Lm = fm.lowered((np.zeros((8, 3), np.float32), kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
-    assert lower.has_active_carry(Lm.it, [0, 1]) and Lm.vg_program((0, 1)) is None
+    assert lower.has_active_carry(Lm.it, [0, 1]) and "_fg" in lower._COMPILED[Lm.vg_program((0, 1)).kernel]
     fq = tm.vmap(quickstart, outputs={"hist": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None), max_steps=100)
     Lq = fq.lowered((np.linspace(0.1, 0.9, 8, dtype=np.float32), prng.split(prng.PRNGKey(0), 8), np.float32(2.0)))
     pq = Lq.vg_program((0,))
     assert [n for n, _, _, _ in pq.result_layout(8)[0]][:4] == ["hist", "ct", "hist.exact", "ct.exact"]
+
+
+def test_forward_mode_value_and_grad_program_for_active_carries():
+    """the mixer's carries depend on a and b: value_and_grad's one-pass program is forward mode (the identity's two
+    tangent lanes contracted with the cotangents at each emit, exact per-item sums)"""
+    kx = prng.split(prng.PRNGKey(3), 8)
+    fm = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), tm.api.torch.int32),
+                                 "end": tm.Sum(())},
+                 in_axes=(0, 0, 0, None, None), max_steps=64)
+    Lm = fm.lowered((np.zeros((8, 3), np.float32), kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
+    p = Lm.vg_program((0, 1))
+    assert p is not None and [t.name for t in p.tallies] == ["dep", "hits", "end", "ct"]
+    names = [n for n, _, _, _ in p.result_layout(8)[0]]
+    assert names == ["dep", "hits", "end", "ct", "ct.exact", "ctl", "stats", "y0", "truncated"]
+    src = lower.jvp_source(Lm.it, [0, 1], 2, contract=True)[0]
+    assert "c.pv.emit(1, a1)" in src and "c.db1_1 = 1.0f;" in src and "c.db1_0 = 0.0f;" in src

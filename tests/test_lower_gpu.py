@@ -430,15 +430,25 @@ def test_lowered_quickstart_onepass_fixed_point(cuda, orc):
     assert np.array_equal(bits(g.cpu().numpy()), bits(orc.q1_grad(x, k, 2.0, np.ones(16, np.float32), C=-1)["g"][0]))
 
 
-def test_lowered_mixer_value_and_grad_uses_replay(cuda):
-    """the mixer's carries depend on a and b: value_and_grad is the forward and the replay"""
-    kx = prng.split(prng.PRNGKey(3), 512)
+@pytest.mark.parametrize("ct", ["end", "dep"])
+def test_lowered_mixer_value_and_grad_forward_mode(cuda, ct):
+    """the mixer's carries depend on a and b: value_and_grad is ONE forward-mode launch (two tangent lanes
+    contracted with the cotangents at each emit); its gradient within the float tolerance of the replay's
+    (exact_order=True), its outputs the forward's"""
+    kx = prng.split(prng.PRNGKey(3), 4096)
     rng = np.random.default_rng(2)
-    pos = rng.uniform(-1, 1, (512, 3)).astype(np.float32)
-    n = rng.integers(1, 40, 512).astype(np.int32)
+    pos = rng.uniform(-1, 1, (4096, 3)).astype(np.float32)
+    n = rng.integers(1, 40, 4096).astype(np.int32)
     f = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), torch.int32), "end": tm.Sum(())},
                 in_axes=(0, 0, 0, None, None), max_steps=64)
-    r, g = f.value_and_grad(pos, kx, n, np.float32(0.3), np.float32(1.7), wrt=(3, 4),
-                            cotangents={"end": torch.ones(())})
+    cts = {"end": torch.ones(())} if ct == "end" else \
+        {"dep": torch.from_numpy(rng.normal(size=(8, 8, 8)).astype(np.float32)), "end": torch.full((), 0.5)}
+    args = (pos, kx, n, np.float32(0.3), np.float32(1.7))
+    r, g = f.value_and_grad(*args, wrt=(3, 4), cotangents=cts)
+    assert B.run.last["kernel"] == f.last_lowered.vg_program((0, 1)).kernel
+    r2, g2 = f.value_and_grad(*args, wrt=(3, 4), cotangents=cts, exact_order=True)
     assert B.run.last["kernel"] == f.last_lowered.grad_program((0, 1)).kernel
-    assert torch.isfinite(g).all()
+    torch.cuda.synchronize()
+    assert near(g.cpu().numpy(), g2.cpu().numpy())
+    assert np.array_equal(r.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
+    assert np.array_equal(np_out(r)["hits"], np_out(r2)["hits"]) and near(np_out(r)["dep"], np_out(r2)["dep"])
