@@ -243,7 +243,8 @@ SH_PI = (Operand("E", (), _F32), Operand("depth", (), _F32), KEY)
 # carries d E / d E0 of its root; csrc/items_shower.cuh SHVG1): per-root exact sums, read out by sh_value_and_grad
 SH_VG1 = ItemProgram("sh_vg_onepass", "sh_vg_onepass", pi=SH_PI,
                      bc=(Operand("X0", (), _F32), Operand("ct_dep", (512,), _F32)), consts=("max_steps", "queue", "items"),
-                     tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32), TSpec("g_E", ("N",), exact=True)),
+                     tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32), TSpec("g_E", ("N",), exact=True),
+                              TSpec("steps", (1,), torch.int64)),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1, spawns=True,
                      queue_leaf_bytes=24)
 SH_REC = ItemProgram("sh_rec", "sh_rec", pi=SH_PI, bc=(Operand("X0", (), _F32),), consts=("max_steps", "queue", "record"),
@@ -477,18 +478,19 @@ def sh_value_and_grad(pi, X0, ct_dep, max_steps=100000, queue=None, stream=None,
     """the shower's forward outputs and the gradient of <ct_dep, dep> in ONE spawn launch (forward mode through
     spawn, SH_VG1), then the per-root readout of the exact words (tm_exact_combine).  d/d depth0 and d/d X0 are
     zero: depth and X0 reach the outputs only through the integer bin index (the tree adjoint gives the same +0).
-    -> dict(dep, count, stats, k, trunc, g_E, g_depth, g_X0) as device tensors (g_E NaN for a root whose sum
-    overflowed; the caller poisons on truncation and dropped children)"""
+    -> dict(dep, count, stats, k, trunc, g_E, g_depth, g_X0, steps: every particle's steps, the launch's work
+    count) as device tensors (g_E NaN for a root whose sum overflowed; the caller poisons on truncation and dropped
+    children)"""
     st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     res = run(SH_VG1, pi, [X0, ct_dep], consts=(max_steps,), queue=queue, stream=st, out=out)
-    dep, count, g_E, stats, k, tr = res
+    dep, count, g_E, steps, stats, k, tr = res
     N = int(k.shape[0])
     if N:
         words = run.last["results"]["g_E.exact"]
         _lib.check(_lib.lib().tm_exact_combine(ctypes.c_void_p(st), ctypes.c_void_p(words.data_ptr()), 1, N,
                                                ctypes.c_void_p(g_E.data_ptr()), ctypes.c_void_p(stats.data_ptr())))
     return dict(dep=dep, count=count, stats=stats, k=k, trunc=tr, g_E=g_E, g_depth=torch.zeros_like(g_E),
-                g_X0=torch.zeros(1, dtype=torch.float32, device=g_E.device))
+                g_X0=torch.zeros(1, dtype=torch.float32, device=g_E.device), steps=steps)
 
 
 def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):

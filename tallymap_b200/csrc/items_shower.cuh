@@ -117,8 +117,10 @@ struct SHFwd {
     if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
     if (o.split) {
       const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
-      o0 = Child{s.E * o.z, s.depth, c0.a, c0.b};
-      o1 = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
+      const Child a{s.E * o.z, s.depth, c0.a, c0.b}, b{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
+      const bool swap = o.z > 0.5f;          // the lower-energy child (the smaller subtree) runs first
+      o0 = swap ? b : a;
+      o1 = swap ? a : b;
       n_out = 2;
     }
   }
@@ -155,7 +157,8 @@ struct SHFwd {
 // each root's gradient is the correctly rounded exact sum of its contributions: the same whatever thread ran which
 // particle.  The same gradient as the tree adjoint, summed differently: within the float tolerance, not bitwise.
 //   sh_vg_onepass  E0, depth0, keys, X0, ct_dep f32[512], consts (max_steps, Q, N), order | dep f32[512], count i32[1],
-//                  g_E f32[N] (read out from the words by the host's exact combine), g_E exact words
+//                  g_E f32[N] (read out from the words by the host's exact combine), steps u64[1] (every
+//                  particle's steps: the work count of the launch), g_E exact words
 //                  u64[5N + (N + 1) / 2], seq, qctl, ctl, stats | k i32[N], trunc u8[N], ring (E, depth, key, tE,
 //                  root)[Q]
 struct ShowerVGChild {
@@ -175,8 +178,8 @@ struct ShowerVGState {
 };
 
 struct SHVG1 {
-  enum { kE0, kDepth0, kKeys, kX0, kCtDep, kConsts, kOrder, kDep, kCount, kGOut, kGE, kSeq, kQctl, kCtl, kStats, kK,
-         kTrunc, kQueue, kNBuf };
+  enum { kE0, kDepth0, kKeys, kX0, kCtDep, kConsts, kOrder, kDep, kCount, kGOut, kSteps, kGE, kSeq, kQctl, kCtl, kStats,
+         kK, kTrunc, kQueue, kNBuf };
   enum { kConstM, kConstQ, kConstN };
   static constexpr int kNB = 512;
   static constexpr int kXOff = kNB * 4 + 16;                       // after the dep bins and the count word
@@ -198,7 +201,9 @@ struct SHVG1 {
     i32* stats;
     i32* kout;
     uint8_t* trunc;
+    unsigned long long* steps;
     mutable i32 n;            // particles this thread finished
+    mutable u32 ns;           // steps this thread ran
     mutable i32 cur;          // the root whose words this thread's slots hold (-1: none)
     mutable ExactPrivS<1> pv;
   };
@@ -218,7 +223,9 @@ struct SHVG1 {
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.kout = static_cast<i32*>(P.p[kK]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
+    c.steps = static_cast<unsigned long long*>(P.p[kSteps]);
     c.n = 0;
+    c.ns = 0u;
     c.cur = -1;
     c.pv.bind(smem + kXOff + ExactBins<1>::kPrivOffset);
   }
@@ -256,6 +263,7 @@ struct SHVG1 {
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
   __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
     const ShowerStepOut o = shower_advance(c.X0, s);
+    c.ns += 1u;
     if (o.low) {
       const i32 b = f2i(s.depth * 8.0f);
       SumPriv<kNB>::emit(c.sh, c.stats, b, s.E);
@@ -269,8 +277,11 @@ struct SHVG1 {
     }
     if (o.split) {
       const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
-      o0 = Child{s.E * o.z, s.depth, c0.a, c0.b, s.tE * o.z, s.root};
-      o1 = Child{s.E * (1.0f - o.z), s.depth, c1.a, c1.b, s.tE * (1.0f - o.z), s.root};
+      const Child a{s.E * o.z, s.depth, c0.a, c0.b, s.tE * o.z, s.root};
+      const Child b{s.E * (1.0f - o.z), s.depth, c1.a, c1.b, s.tE * (1.0f - o.z), s.root};
+      const bool swap = o.z > 0.5f;          // the lower-energy child (the smaller subtree) runs first
+      o0 = swap ? b : a;
+      o1 = swap ? a : b;
       n_out = 2;
     }
   }
@@ -286,6 +297,7 @@ struct SHVG1 {
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
     merge(c);
+    if (c.ns) atomicAdd(c.steps, (unsigned long long)c.ns);
     SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.dep, tid, nth);
     if (c.n) atomicAdd(c.shc, c.n);
     __syncthreads();

@@ -80,7 +80,7 @@ void add_spawn(const char* name) {
   k.name = name;
   k.fn = reinterpret_cast<const void*>(&tmb::spawn_kernel<I>);
   k.nbuf = I::kNBuf;
-  k.smem = I::kSmemBytes;
+  k.smem = tmb::SpawnSmem<I>::kBytes;         // the item's block, then the lanes' shared stack entries
   (*g_reg)[name_id(name)] = k;
   g_names->push_back(name);
 }

@@ -10,10 +10,11 @@
 // for ticket t, slot t % Q, lap L = t / Q, the slot is free for L when seq == 2L, published when 2L + 1, and freed to
 // 2L + 2 by its consumer.  Control words sit on separate 128-byte lines (the reference's QCTL_STRIDE, kernel.py:307).
 //
-// Work sharing: a lane keeps the children it spawns on a private stack (kPrivate entries in local memory) and runs
-// them depth-first, with no atomics, unless lanes are hungry: a lane that finds no work counts itself in the hungry
-// word until it gets some, and a lane that spawns shares its children through the ring while the ring holds fewer
-// pending children than there are hungry lanes.  So the ring carries only the children other lanes are waiting for.  A breadth-first FIFO over 10^6 roots
+// Work sharing: a lane keeps the children it spawns on a private stack (its newest entries in shared memory, older
+// ones in local memory) and runs them depth-first, with no atomics, unless lanes are hungry: a lane that finds no
+// work counts itself in the hungry word until it gets some, and a lane that spawns shares its children through the
+// ring while the ring holds fewer pending children than there are hungry lanes (looked at every 16 iterations while
+// not sharing, every iteration while sharing).  So the ring carries only the children other lanes are waiting for.  A breadth-first FIFO over 10^6 roots
 // would need a ring as wide as the whole forest's frontier (the reference sizes its Queue to the pending children);
 // depth-first lanes share only what hungry lanes wait for, so the ring never overflows and a count is deterministic.
 // in a different order than the reference's ring runs them, which changes no tally bit beyond float summation order.
@@ -37,6 +38,18 @@ enum { kQTail = 0, kQHead = 1, kQPending = 2, kQOcc = 3, kQFlight = 4, kQHungry 
 constexpr u32 kSpinLimit = 1u << 22;   // polls of a slot sequence word (~0.3 s with the back-off)
 constexpr u64 kIdleLimitNs = 20000000000ull;   // 20 s without progress: give up (the error word says so)
 constexpr int kPrivate = 48;       // a lane's private stack of children (a shower's tree is < 80 generations deep)
+constexpr int kStackShared = 6;    // its newest entries live in the thread's column of shared memory
+
+// A lane's private children: a stack whose newest entries (up to kStackShared) are in shared memory (word w of entry
+// e of thread t at u32 [(e * W + w) * TM_BLOCK + t]: conflict-free whatever entry each lane touches); when they are
+// all taken, they move to local memory together.  In local memory alone, the lanes' different stack depths put
+// every lane's word in its own sector, and the stacks of a full SM overflow L1 into L2 and DRAM.
+template <class I>
+struct SpawnSmem {
+  static constexpr int kCW = (int)(sizeof(typename I::Child) / 4);
+  static constexpr int kItemBytes = (I::kSmemBytes + 15) / 16 * 16;
+  static constexpr int kBytes = kItemBytes + kStackShared * kCW * 4 * TM_BLOCK;
+};
 
 __device__ __forceinline__ u32* qword(u32* q, int w) { return q + w * kQStride; }
 __device__ __forceinline__ u32 ld_volatile(const u32* p) { return *reinterpret_cast<const volatile u32*>(p); }
@@ -71,7 +84,9 @@ __device__ __forceinline__ bool wait_seq(const u32* seq, u32 slot, u32 want) {
 //   kQueue, kSeq, kQctl        buffer indices of the ring (Child[Q]), its sequence words (u32[Q]) and control words
 //   kConstQ                    index of Q in the launch constants
 //   start_child(Ctx&, const Child&) -> State       a popped child's pre-loop code
-//   step(const Ctx&, State&, Child& o0, Child& o1, int& n_out)   one step; up to 2 children to spawn
+//   step(const Ctx&, State&, Child& o0, Child& o1, int& n_out)   one step; up to 2 children to spawn (kept
+//                              privately, o0 runs first: an item that puts its smaller subtree in o0 keeps the
+//                              private stack shallow)
 //   finish(const Ctx&, const State&, i64 item, bool child)   post-loop code; per-item results for roots only
 // or, with kPostSpawn = true (children spawned after the loop, tallymap/_tally.py spawn in the post-loop code):
 //   finish(const Ctx&, const State&, i64 item, bool child, Child& o0, Child& o1, int& n_out)
@@ -106,13 +121,45 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
   bool active = false, alive = true, child = false, roots_left = true, hungry = false;
   u64 idle_since = 0;
   u32 spawned = 0;                  // this thread's spawned children, added to stats[0] once at the end
-  Child stk[kPrivate];
-  int ns = 0;
+  static_assert(sizeof(Child) % 4 == 0, "a child is whole 4-byte words");
+  constexpr int kCW = SpawnSmem<I>::kCW;
+  union ChildWords {
+    Child c;
+    u32 w[kCW];
+  };
+  u32* const sstk = reinterpret_cast<u32*>(smem + SpawnSmem<I>::kItemBytes) + threadIdx.x;
+  int sn = 0;                       // entries in shared memory (the newest)
+  u32 iter = 0u;
+  bool share_c = false;             // the sharing decision, refreshed every 16 iterations
+  Child stk[kPrivate];              // older entries, moved here kStackShared at a time when the shared part is full
+  int nl = 0;
+  auto sput = [&](int e, const Child& ch) {
+    ChildWords u;
+    u.c = ch;
+#pragma unroll
+    for (int j = 0; j < kCW; ++j) sstk[(e * kCW + j) * TM_BLOCK] = u.w[j];
+  };
+  auto sget = [&](int e) {
+    ChildWords u;
+#pragma unroll
+    for (int j = 0; j < kCW; ++j) u.w[j] = sstk[(e * kCW + j) * TM_BLOCK];
+    return u.c;
+  };
+  auto has_room = [&]() { return sn < kStackShared || nl + kStackShared <= kPrivate; };
+  auto push = [&](const Child& ch) {          // (has_room() holds)
+    if (sn == kStackShared) {
+      for (int e = 0; e < kStackShared; ++e) stk[nl + e] = sget(e);
+      nl += kStackShared;
+      sn = 0;
+    }
+    sput(sn++, ch);
+  };
+  auto pop = [&]() { return sn > 0 ? sget(--sn) : stk[--nl]; };   // (a private child exists)
   for (;;) {
     // ---- lanes without an item: their own children first, then the ring's, then roots
     bool needy = alive && !active;
-    if (needy && ns > 0) {
-      x = I::start_child(cx, stk[--ns]);
+    if (needy && (sn > 0 || nl > 0)) {
+      x = I::start_child(cx, pop());
       child = true;
       active = true;
       needy = false;
@@ -225,16 +272,21 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
     }
     // ---- spawned children: onto the private stack unless lanes are hungry for them (or the stack is full), else
     // into the ring, warp-aggregated
+    // whether to share: while not sharing, re-read every 16 iterations (warp-uniform, one load per warp), not at
+    // every spawn -- a load of the two control words at every spawn put an L2 round trip on the path of nearly every
+    // iteration; while sharing (the launch's tail), every iteration, so that sharing stops as soon as the ring holds
+    // what the hungry lanes wait for.  The decision is a policy: it changes no count and no termination.
+    if (share_c || (++iter & 15u) == 0u)
+      share_c = (i32)ld_volatile(qword(q, kQPending)) < (i32)ld_volatile(qword(q, kQHungry));
     if (n_out > 0) {
       spawned += (u32)n_out;
-      const bool share =
-          (i32)ld_volatile(qword(q, kQPending)) < (i32)ld_volatile(qword(q, kQHungry));
+      const bool share = share_c;
       int ng = 0;
-      if (!share && ns < kPrivate) stk[ns++] = o0;
+      if (!share && has_room()) push(o0);
       else ng = 1;
       if (n_out > 1) {
-        if (!share && ns < kPrivate) {
-          stk[ns++] = o1;
+        if (!share && has_room()) {
+          push(o1);
         } else {
           if (ng == 0) o0 = o1;
           ++ng;
@@ -288,7 +340,7 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
     if (done) {
       if constexpr (!post_spawn_trait<I>::value) I::finish(cx, x, item, child);
       active = false;
-      if (ns == 0) {                 // busy -> idle: leave the in-flight count
+      if (sn == 0 && nl == 0) {                  // busy -> idle: leave the in-flight count
         __threadfence();
         atomicSub(qword(q, kQFlight), 1u);
       }

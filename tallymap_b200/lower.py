@@ -28,6 +28,7 @@ from . import trace as T
 CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
 PRIV_BYTES = 4096        # outputs up to this size are privatised per block in shared memory (kernel.py:300)
 CTYPE = {T.F32: "float", T.I32: "i32", T.U32: "u32", T.BOOL: "bool"}
+SPAWN_STACK_SHARED = 6   # a lane's private stack entries in shared memory (csrc/tm_spawn.cuh kStackShared)
 TDTYPE = {T.F32: torch.float32, T.I32: torch.int32, T.U32: torch.int32, T.BOOL: torch.uint8}
 
 
@@ -991,6 +992,10 @@ class Lowered:
         nrec = sum(len(fl) + 3 for _, _, fl in records)
         sp = it.spawns
         nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys) + (3 if sp else 0)
+        if sp:
+            # the spawn runtime's shared stack entries after the item's block (csrc/tm_spawn.cuh SpawnSmem)
+            smem = (smem + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * len(it.loads) * 128
+            src += f"\nstatic_assert(tmb::SpawnSmem<tmb::GenFwd>::kBytes == {smem}, \"shared-memory size\");"
         kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc,
                                consts=("max_steps", "queue") if sp else ("max_steps",), tallies=tallies,

@@ -154,6 +154,7 @@ def test_sh_vg_onepass(cuda, orc, n):
     B.check_status(B.run.last["ctl"])
     ref = orc.sh_fwd(*inp)
     assert np.array_equal(r["count"].cpu().numpy(), ref["count"])
+    assert int(r["steps"][0]) >= int(r["count"][0]) + int(ref["k"].sum()) - n      # every particle steps once
     assert np.array_equal(r["k"].cpu().numpy(), ref["k"])
     assert np.array_equal(r["stats"].cpu().numpy(), ref["stats"])
     assert np.abs(r["dep"].cpu().numpy().astype(np.float64) - ref["dep"]).max() <= FT * np.abs(ref["dep"]).max()
