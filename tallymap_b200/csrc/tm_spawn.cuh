@@ -353,7 +353,9 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
 }
 
 template <class I>
-__global__ void __launch_bounds__(TM_BLOCK) spawn_kernel(const Params P, const i64 n_items) {
+// (at least 6 blocks per SM: ptxas then keeps the loop's values in up to 80 registers instead of spilling them at
+// the 64-72 it picks unbounded; the shower's step 105 -> 95 ms, 5 blocks gave the same)
+__global__ void __launch_bounds__(TM_BLOCK, 6) spawn_kernel(const Params P, const i64 n_items) {
   spawn_body<I>(P, n_items);
 }
 
