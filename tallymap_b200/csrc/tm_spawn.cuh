@@ -38,7 +38,7 @@ enum { kQTail = 0, kQHead = 1, kQPending = 2, kQOcc = 3, kQFlight = 4, kQHungry 
 constexpr u32 kSpinLimit = 1u << 22;   // polls of a slot sequence word (~0.3 s with the back-off)
 constexpr u64 kIdleLimitNs = 20000000000ull;   // 20 s without progress: give up (the error word says so)
 constexpr int kPrivate = 48;       // a lane's private stack of children (a shower's tree is < 80 generations deep)
-constexpr int kStackShared = 6;    // its newest entries live in the thread's column of shared memory
+constexpr int kStackShared = 8;    // its newest entries live in the thread's column of shared memory
 
 // A lane's private children: a stack whose newest entries (up to kStackShared) are in shared memory (word w of entry
 // e of thread t at u32 [(e * W + w) * TM_BLOCK + t]: conflict-free whatever entry each lane touches); when they are

@@ -28,7 +28,7 @@ from . import trace as T
 CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
 PRIV_BYTES = 4096        # outputs up to this size are privatised per block in shared memory (kernel.py:300)
 CTYPE = {T.F32: "float", T.I32: "i32", T.U32: "u32", T.BOOL: "bool"}
-SPAWN_STACK_SHARED = 6   # a lane's private stack entries in shared memory (csrc/tm_spawn.cuh kStackShared)
+SPAWN_STACK_SHARED = 8   # a lane's private stack entries in shared memory (csrc/tm_spawn.cuh kStackShared)
 TDTYPE = {T.F32: torch.float32, T.I32: torch.int32, T.U32: torch.int32, T.BOOL: torch.uint8}
 
 
