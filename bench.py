@@ -47,6 +47,7 @@ METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
 # under profiles/ (kernel -> (bytes per item, items in the capture)); the bench scales them to its own launch
 TRAFFIC = {
     "rw_vg_onepass": ((52342272 + 2833664) / 4194304, 4194304),
+    "ph_vg_onepass": ((36617472 + 297728) / 4194304, 4194304),
     "rw_vg": ((38916657408 + 37082540288) / 4194304, 4194304),
     "rw_grad": ((5.241173e9 + 6.034955e9) / 1048576, 1048576),
     "rw_fwd": ((53075712 + 3524096) / 4194304, 4194304),
