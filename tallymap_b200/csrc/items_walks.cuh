@@ -25,6 +25,8 @@
 
 namespace tmb {
 
+// kc: the retrace counter (the loop's steps so far, capped by max_steps); the item's own step counter k equals it
+// (both start at 0 and gain 1 per step), so one register holds both
 struct WalkState {
   i32 kc, k;
   float x;
@@ -72,14 +74,13 @@ struct Q1Fwd : Q1Common {
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
   __device__ __forceinline__ static void step(const Ctx& c, State& s) {
-    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    const float u = uniform01(fold_in(c.key, (u32)s.kc));
     SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.x * 16.0f), c.theta * (1.0f - s.x));
     s.kc += 1;
-    s.k += 1;
     s.x = s.x * (0.5f + 0.5f * u);
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item) {
-    c.kout[item] = s.k;
+    c.kout[item] = s.kc;
     c.trunc[item] = (s.kc >= c.M && pred(s.x)) ? 1 : 0;
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
@@ -140,9 +141,8 @@ struct Q1Grad : Q1Common {
     return State{(i32)step, (i32)step, x};
   }
   __device__ __forceinline__ static void fwd(const Ctx& c, State& s) {
-    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    const float u = uniform01(fold_in(c.key, (u32)s.kc));
     s.kc += 1;
-    s.k += 1;
     s.x = s.x * (0.5f + 0.5f * u);
   }
   __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {
@@ -208,15 +208,14 @@ struct RWFwd : RWCommon {
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
   __device__ __forceinline__ static void step(const Ctx& c, State& s) {
-    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    const float u = uniform01(fold_in(c.key, (u32)s.kc));
     SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.x * 256.0f), c.drift * s.x);
     s.kc += 1;
-    s.k += 1;
     s.x = move(s.x, u);
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item) {
     SumPriv<2>::emit(c.sh + kNB, c.stats, s.x > 1.0f ? 1 : 0, 1.0f);
-    c.kout[item] = s.k;
+    c.kout[item] = s.kc;
     c.trunc[item] = (s.kc >= c.M && pred(s.x)) ? 1 : 0;
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
@@ -278,9 +277,8 @@ struct RWGrad : RWCommon {
     return State{(i32)step, (i32)step, x};
   }
   __device__ __forceinline__ static void fwd(const Ctx& c, State& s) {
-    const float u = uniform01(fold_in(c.key, (u32)s.k));
+    const float u = uniform01(fold_in(c.key, (u32)s.kc));
     s.kc += 1;
-    s.k += 1;
     s.x = move(s.x, u);
   }
   __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {

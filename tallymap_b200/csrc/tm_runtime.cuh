@@ -114,6 +114,12 @@ __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items)
       }
     }
     if (!__any_sync(0xffffffffu, alive)) break;
+    // while every lane's item steps, steps run back to back without the claim and finish checks, until one ends
+    if (__all_sync(0xffffffffu, active && I::cond(cx, x))) {
+      do {
+        I::step(cx, x);
+      } while (__all_sync(0xffffffffu, I::cond(cx, x)));
+    }
     const bool stepping = alive && I::cond(cx, x);
     __syncwarp();
     if (stepping) {
