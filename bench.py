@@ -501,6 +501,15 @@ def main():
                         (f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
                          f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
                          "steps from the per-item trip counts and the replay schedule)")} if cfg.tf else None
+    if roofline is not None and traffic is not None:
+        # the memory side of the roofline: the kernel's measured DRAM bytes per launch over its time, against the
+        # measured copy bandwidth (MEASURED_PEAKS.json): how far from memory-bound the path is
+        mp = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+        hbm = json.load(open(mp)).get("hbm_gbs") if os.path.exists(mp) else None
+        gbs = traffic / (dom[2] / 1e3) / 1e9
+        roofline["hbm"] = {"achieved": round(gbs, 2), "unit": "GB/s", "peak": hbm,
+                           "frac": round(gbs / hbm, 5) if hbm else None,
+                           "peak_source": "measured: MEASURED_PEAKS.json hbm_gbs" if hbm else None}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
