@@ -466,7 +466,8 @@ class MappedFn:
             raise ValueError(f"tallymap_b200: at most {lower.LANES_MAX} tangent lanes per launch")
         prog = L_.jvp_program(bpos, L)
         pi, bc = self._split(args)
-        out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,))
+        out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,),
+                    queue=self.spawn.capacity if self.spawn else None)
         nf = len(L_.fwd.tallies)
         nt = len(prog.tallies)
         tallies = {t.name: v for t, v in zip(prog.tallies[:nf], out[:nf])}
@@ -478,8 +479,9 @@ class MappedFn:
         n_tr = trunc.sum(dtype=torch.int32)
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
-        res = Result(_poison(tallies, n_tr > 0), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
-        dts = _poison(dts, n_tr > 0)
+        bad = _limits(prog, stats)
+        res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        dts = _poison(dts, bad)
         if not lanes_given:
             dts = {k: v[0] for k, v in dts.items()}
         return res, dts
@@ -516,7 +518,8 @@ class MappedFn:
                 continue
             c = cotangents.get(name)
             cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
-        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,))
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,),
+                    queue=self.spawn.capacity if self.spawn else None)
         nt = len(L.fwd.tallies)
         tallies = {t.name: v for t, v in zip(L.fwd.tallies, out[:nt])}
         ct = out[nt].reshape(-1)

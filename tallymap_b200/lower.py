@@ -565,10 +565,11 @@ def compile_kernel(source, note, n_buffers, smem_bytes):
 
 
 # ------------------------------------------------------------------------------------------------ reverse program
-def _active(it, wrt):
-    """float variables that depend on the differentiated broadcast operands (tallymap/_reverse.py:208 `_active`)"""
+def _active(it, wrt, extra=()):
+    """float variables that depend on the differentiated broadcast operands (tallymap/_reverse.py:208 `_active`);
+    extra: more seeds (a spawning item's float per-item inputs: a child's may carry tangents)"""
     tr = it.tr
-    act = {it.bc[k].id for k in wrt if it.bc[k].dtype == T.F32}
+    act = {it.bc[k].id for k in wrt if it.bc[k].dtype == T.F32} | set(extra)
 
     def prop(eqns):
         for e in eqns:
@@ -1018,18 +1019,24 @@ class Lowered:
             if self.it.exact or self.fwd.records:
                 raise NotImplementedError("tallymap_b200: forward mode of fixed_point or Records outputs is not "
                                           "lowered")
-            if self.it.spawns:
-                raise NotImplementedError("tallymap_b200: forward mode through spawn is not lowered for traced items")
             src, smem = jvp_source(self.it, list(wrt), int(lanes))
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
             tallies = self.fwd.tallies + tuple(TSpec("d_" + nm, (int(lanes),) + tuple(shape)) for nm, shape in fts)
             tallies = tuple(dataclasses.replace(t, exact=False) for t in tallies)
-            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 2 + len(self.fwd.ys)
+            sp = self.it.spawns
+            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 2 + len(self.fwd.ys) + (3 if sp else 0)
             kid = compile_kernel(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
-            self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc, consts=("max_steps",),
-                                         tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
+            self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc,
+                                         consts=("max_steps", "queue") if sp else ("max_steps",),
+                                         tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc, spawns=sp,
+                                         queue_leaf_bytes=self._child_bytes(int(lanes)) if sp else 0)
         return self.jvps[key]
+
+    def _child_bytes(self, L):
+        """bytes of a child of this spawning item in a forward-mode program: its leaves and L tangents of each float
+        leaf"""
+        return 4 * (len(self.it.loads) + L * sum(1 for v, _ in self.it.loads if v.dtype == T.F32))
 
     def vg_program(self, wrt):
         """the one-pass value-and-grad program for bc[wrt] (forward outputs, then the exact cotangent tally): with no
@@ -1040,23 +1047,29 @@ class Lowered:
         wrt = tuple(wrt)
         if wrt not in self.vgs:
             prog = None
-            if not (self.fwd.records or self.it.spawns):
-                self.grad_program(wrt)            # (the same checks)
+            sp = self.it.spawns
+            if not self.fwd.records:
+                for k in wrt:
+                    if self.bc[k].dtype != torch.float32:
+                        raise LowerError("tallymap_b200.lower: only float32 broadcast operands are differentiable")
                 fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
                 bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
                 tallies = self.fwd.tallies + (TSpec("ct", (len(wrt),), exact=True),)
-                if not has_active_carry(self.it, list(wrt)):
+                if not sp and not has_active_carry(self.it, list(wrt)):
                     src, smem, nbuf = onepass_source(self.it, list(wrt))
                     kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
                 elif len(wrt) <= FWD_GRAD_MAX and not self.it.exact:
+                    # forward mode; through spawn, each child carries its float leaves' tangents
                     src, smem = jvp_source(self.it, list(wrt), len(wrt), contract=True)
-                    nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 1 + 2 + len(self.fwd.ys)
+                    nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 1 + 2 + len(self.fwd.ys) + (3 if sp else 0)
                     kid = compile_kernel(src, f"{self.name}_fg{''.join(map(str, wrt))}", nbuf, smem)
                 else:
                     kid = None
                 if kid is not None:
-                    prog = ItemProgram(f"{self.name}_vg", kid, pi=self.pi, bc=bc, consts=("max_steps",),
-                                       tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
+                    prog = ItemProgram(f"{self.name}_vg", kid, pi=self.pi, bc=bc,
+                                       consts=("max_steps", "queue") if sp else ("max_steps",),
+                                       tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc, spawns=sp,
+                                       queue_leaf_bytes=self._child_bytes(len(wrt)) if sp else 0)
             self.vgs[wrt] = prog
         return self.vgs[wrt]
 
@@ -1148,11 +1161,17 @@ def _jvp_rule(e, a, d, out):
     raise LowerError(f"tallymap_b200.lower: no jvp rule for {p}")
 
 
-def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "):
-    """straight-line primal code with each active value's L tangents; tnames: id -> [L tangent expressions]"""
+def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    ", spawner=None):
+    """straight-line primal code with each active value's L tangents; tnames: id -> [L tangent expressions];
+    spawner(when, leaves, leaf tangents): a spawn with its children's tangents"""
     out = []
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        if e.prim == "spawn":
+            if spawner is not None:
+                tl = [tnames.get(x.id) if isinstance(x, T.Var) else None for x in e.ins[1:]]
+                out.append(indent + spawner(a[0], a[1:], tl))
+            continue
         out += _emit_code([e], names, emitter, indent)
         if e.prim == "emit":
             v = e.ins[1]
@@ -1190,9 +1209,12 @@ def jvp_source(it, wrt, L, contract=False):
         L = W
     if not 1 <= L <= LANES_MAX:
         raise LowerError(f"tallymap_b200.lower: 1..{LANES_MAX} tangent lanes")
-    act, carry_act = _active(it, wrt)
+    sp = it.spawns
+    # a spawning item: a child carries its float per-item inputs' tangents (fl: their positions among the leaves)
+    fl = [m for m, (v, _) in enumerate(it.loads) if v.dtype == T.F32] if sp else []
+    act, carry_act = _active(it, wrt, extra=[it.loads[m][0].id for m in fl])
     ftal = [(t, name, shape) for t, (name, (shape, dt)) in enumerate(it.specs) if dt == T.F32]
-    lines = [PRELUDE, "namespace tmb {", "struct GenJvp {"]
+    lines = [('#include "tm_spawn.cuh"' if sp else "") + PRELUDE, "namespace tmb {", "struct GenJvp {"]
     idx = 0
     enum = []
     for j in range(npi):
@@ -1214,13 +1236,25 @@ def jvp_source(it, wrt, L, contract=False):
     else:
         for q, _ in enumerate(ftal):
             enum.append(f"kD{q} = {idx}"); idx += 1
+    if sp:
+        enum.append(f"kSeq = {idx}"); idx += 1
+        enum.append(f"kQctl = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
         enum.append(f"kY{r} = {idx}"); idx += 1
     enum.append(f"kTrunc = {idx}"); idx += 1
+    if sp:
+        enum.append(f"kQueue = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
+    if sp:
+        lines.append("  enum { kConstM, kConstQ };")
+        fields = [f"{CTYPE[v.dtype]} l{m};" for m, (v, _) in enumerate(it.loads)]
+        fields += [f"float d{m}_{l};" for m in fl for l in range(L)]
+        lines.append("  struct Child { " + " ".join(fields) + " };")
+        if it.post_spawns:
+            lines.append("  static constexpr bool kPostSpawn = true;")
     smem, priv = 0, {}
     if contract:
         # the exact cotangent bins with the threads' private words first, then the staged output cotangents
@@ -1359,33 +1393,49 @@ def jvp_source(it, wrt, L, contract=False):
         return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) fatom(&{tgt}[{l * S} + b_], {dv_c}); }}"
 
     bc_t = {it.bc[k].id: [f"c.db{k}_{l}" for l in range(L)] for k in wrt}
-    # start
-    lines.append("  __device__ static State start(Ctx& c, i64 item) {")
-    names = _names_pre(it)
-    tn = dict(bc_t)
-    if contract:
-        acc["p"] = "a"
-        for l in range(L):
-            lines.append(f"    float a{l} = 0.0f;")
-    for v, ld in it.loads:
-        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
-    lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter)
-    for i in it.saved:
-        lines.append(f"    c.p{i} = {names[i]};")
-    for i in act_saved:
-        for l in range(L):
-            lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
-    lines += ["    State s;", "    s.kc = 0;"]
-    if contract:
-        for l in range(L):
-            lines.append(f"    s.a{l} = a{l};")
-    for j, x in enumerate(tr.carry_in):
-        lines.append(f"    s.c{j} = {_ref(x, names)};")
-        if carry_act[j]:
+
+    def spawner(when_c, leaves_c, leaf_t):
+        """a child's leaves and, for its float leaves, their tangents"""
+        st = [f"if ({when_c}) {{ Child& o_ = n_out == 0 ? o0 : o1;"]
+        st += [f" o_.l{m} = {v};" for m, v in enumerate(leaves_c)]
+        for m in fl:
             for l in range(L):
-                tv = tn[x.id][l] if isinstance(x, T.Var) and x.id in tn else "0.0f"
-                lines.append(f"    s.d{j}_{l} = {tv};")
-    lines += ["    return s;", "  }"]
+                st.append(f" o_.d{m}_{l} = {leaf_t[m][l] if leaf_t[m] is not None else '0.0f'};")
+        st.append(" ++n_out; }")
+        return "".join(st)
+    # start (a root: its inputs carry no tangent) and start_child (a child's leaves and their tangents)
+    heads = [("State start(Ctx& c, i64 item)", [ld for _, ld in it.loads], {})]
+    if sp:
+        heads.append(("State start_child(Ctx& c, const Child& ch)", [f"ch.l{m}" for m in range(len(it.loads))],
+                      {it.loads[m][0].id: [f"ch.d{m}_{l}" for l in range(L)] for m in fl}))
+    for head, src_, tin in heads:
+        lines.append(f"  __device__ static {head} {{")
+        names = _names_pre(it)
+        tn = dict(bc_t)
+        tn.update(tin)
+        if contract:
+            acc["p"] = "a"
+            for l in range(L):
+                lines.append(f"    float a{l} = 0.0f;")
+        for (v, _), ld in zip(it.loads, src_):
+            lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+        lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter)
+        for i in it.saved:
+            lines.append(f"    c.p{i} = {names[i]};")
+        for i in act_saved:
+            for l in range(L):
+                lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
+        lines += ["    State s;", "    s.kc = 0;"]
+        if contract:
+            for l in range(L):
+                lines.append(f"    s.a{l} = a{l};")
+        for j, x in enumerate(tr.carry_in):
+            lines.append(f"    s.c{j} = {_ref(x, names)};")
+            if carry_act[j]:
+                for l in range(L):
+                    tv = tn[x.id][l] if isinstance(x, T.Var) and x.id in tn else "0.0f"
+                    lines.append(f"    s.d{j}_{l} = {tv};")
+        lines += ["    return s;", "  }"]
     lines += _pred_fn(it)
     lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
     lines.append("    return s.kc < c.M && pred(c, s);")
@@ -1399,11 +1449,15 @@ def jvp_source(it, wrt, L, contract=False):
             if carry_act[j]:
                 tn[v.id] = [f"{state}.d{j}_{l}" for l in range(L)]
         return tn
-    lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
+    if sp:
+        lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, "
+                     "int& n_out) {")
+    else:
+        lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
     names = _names_loop(it, tr.carry)
     tn = loop_tn(tr.carry, "s")
     acc["p"] = "s.a"
-    lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter)
+    lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter, spawner=spawner)
     for j, x in enumerate(tr.body_out):
         lines.append(f"    const {CTYPE[tr.carry[j].dtype]} n{j} = {_ref(x, names)};")
         if carry_act[j]:
@@ -1416,20 +1470,30 @@ def jvp_source(it, wrt, L, contract=False):
             for l in range(L):
                 lines.append(f"    s.d{j}_{l} = nd{j}_{l};")
     lines += ["    s.kc += 1;", "  }"]
-    lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    if not sp:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
+    elif it.post_spawns:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child, Child& o0, "
+                     "Child& o1, int& n_out) {")
+    else:
+        lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item, bool child) {")
     names = _names_loop(it, tr.post_carry)
     tn = loop_tn(tr.post_carry, "s")
     if contract:
         acc["p"] = "a"
         for l in range(L):
             lines.append(f"    float a{l} = s.a{l};")
-    lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter)
+    lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter, spawner=spawner)
     if contract:
         for l in range(L):
             lines.append(f"    if (c.pv.emit({l}, a{l})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
+    if sp:
+        # a child's per-item results are discarded (tallymap/_tally.py:285-286); its truncation is counted
+        lines.append("    const bool tr_ = s.kc >= c.M && pred(c, s);")
+        lines.append("    if (child) { if (tr_) atomicAdd(&c.stats[kStChildrenTruncated], 1); return; }")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
-    lines.append("    c.trunc[item] = (s.kc >= c.M && pred(c, s)) ? 1 : 0;")
+    lines.append("    c.trunc[item] = " + ("tr_ ? 1 : 0;" if sp else "(s.kc >= c.M && pred(c, s)) ? 1 : 0;"))
     lines.append("  }")
     lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")
     if contract:
@@ -1454,7 +1518,12 @@ def jvp_source(it, wrt, L, contract=False):
     lines.append("};")
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
-    lines.append("  tmb::forward_body<tmb::GenJvp>(P, n);")
+    lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenJvp>(P, n);")
     lines.append("}")
     lines.append(f"static_assert(tmb::GenJvp::kSmemBytes == {max(smem, 16)}, \"shared-memory size\");")
-    return "\n".join(lines), max(smem, 16)
+    total = max(smem, 16)
+    if sp:
+        # the spawn runtime's shared stack entries after the item's block (csrc/tm_spawn.cuh SpawnSmem)
+        total = (total + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * (len(it.loads) + len(fl) * L) * 128
+        lines.append(f"static_assert(tmb::SpawnSmem<tmb::GenJvp>::kBytes == {total}, \"shared-memory size\");")
+    return "\n".join(lines), total

@@ -115,3 +115,17 @@ def spawn_walk(t, g, x, key):
     k, w, t = tl.while_loop(lambda c: c[0] < n, body, (0, x, t))
     t = t.spawn((g + 1, w * 1.25, tl.random.fold_in(key, 7)), when=g < 3)
     return t, k
+
+
+def spawn_decay(t, g, w, key, a):
+    """three steps per item, each depositing a * w * u; a child (generation g + 1) with weight w * a after the loop
+    while g < 2: the outputs are polynomials in the broadcast a (degree <= 3), so a central difference is exact up to
+    its third-order term"""
+    def body(c):
+        k, w, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("Q", k % 8, a * w * u)
+        return k + 1, w * 0.9, t
+    k, w, t = tl.while_loop(lambda c: c[0] < 3, body, (0, w, t))
+    t = t.spawn((g + 1, w * a, tl.random.fold_in(key, 7)), when=g < 2)
+    return t, k

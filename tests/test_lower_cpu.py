@@ -235,3 +235,17 @@ def test_forward_mode_value_and_grad_program_for_active_carries():
     assert names == ["dep", "hits", "end", "ct", "ct.exact", "ctl", "stats", "y0", "truncated"]
     src = lower.jvp_source(Lm.it, [0, 1], 2, contract=True)[0]
     assert "c.pv.emit(1, a1)" in src and "c.db1_1 = 1.0f;" in src and "c.db1_0 = 0.0f;" in src
+
+
+def test_forward_mode_through_spawn_lowers():
+    """a spawning item's forward-mode programs: the child carries its float leaves' tangents"""
+    from items_lang import spawn_decay
+    f = tm.vmap(spawn_decay, outputs={"Q": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=10,
+                spawn=tm.Queue(4096))
+    L = f.lowered((np.zeros(4, np.int32), np.ones(4, np.float32), prng.split(prng.PRNGKey(2), 4), np.float32(1.1)))
+    p = L.vg_program((0,))
+    assert p.spawns and p.queue_leaf_bytes == 4 * (4 + 1) and p.consts == ("max_steps", "queue")
+    src = lower.jvp_source(L.it, [0], 1, contract=True)[0]
+    assert "float d1_0;" in src and "start_child(Ctx& c, const Child& ch)" in src and "spawn_body<tmb::GenJvp>" in src
+    j = L.jvp_program((0,), 2)
+    assert j.spawns and j.queue_leaf_bytes == 4 * (4 + 2)

@@ -452,3 +452,42 @@ def test_lowered_mixer_value_and_grad_forward_mode(cuda, ct):
     assert near(g.cpu().numpy(), g2.cpu().numpy())
     assert np.array_equal(r.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
     assert np.array_equal(np_out(r)["hits"], np_out(r2)["hits"]) and near(np_out(r)["dep"], np_out(r2)["dep"])
+
+
+# ---------------------------------------------------------------------------------------------- forward mode through spawn
+def _decay_args(n=3000):
+    rng = np.random.default_rng(12)
+    return (np.zeros(n, np.int32), rng.uniform(0.5, 1.5, n).astype(np.float32), prng.split(prng.PRNGKey(13), n))
+
+
+def _decay_eval(args, a):
+    from items_lang import spawn_decay
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    tr = T.trace_item(spawn_decay, ["i32", "f32", "key", "f32"], 3, {"Q": ((8,), "f32")}, spawn=True)
+    return Evaluator(tr, 10).run(list(args), [np.float32(a)])
+
+
+def test_forward_mode_through_spawn(cuda):
+    """value_and_grad and jvp of a spawning item w.r.t. a broadcast operand: children carry their weight's tangent;
+    against a central difference of the IR evaluator (the outputs are polynomials of degree <= 3 in a)"""
+    from items_lang import spawn_decay
+    args = _decay_args()
+    a, h = 1.1, 1.1e-2
+    f = tm.vmap(spawn_decay, outputs={"Q": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=10,
+                spawn=tm.Queue(1 << 16))
+    ct = np.linspace(-1.0, 2.0, 8).astype(np.float32)
+    r, g = f.value_and_grad(*args, np.float32(a), wrt=3, cotangents={"Q": torch.from_numpy(ct)})
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    assert int(r.stats["spawned"]) == 2 * len(args[0])
+    qp, qm = _decay_eval(args, a + h)["sums"]["Q"], _decay_eval(args, a - h)["sums"]["Q"]
+    dq = (qp - qm) / (2 * h)
+    want = float(np.dot(ct.astype(np.float64), dq))
+    assert abs(float(g) - want) <= 1e-3 * np.abs(ct.astype(np.float64) * dq).sum()
+    q0 = _decay_eval(args, a)["sums"]["Q"]
+    assert near(np_out(r)["Q"], q0)
+    # forward mode with a tangent tally: the same derivative per bin
+    _, dts = f.jvp(*args, np.float32(a), wrt=3, tangents=[1.0])
+    torch.cuda.synchronize()
+    assert np.abs(dts["Q"].cpu().numpy() - dq).max() <= 1e-3 * np.abs(dq).max()
