@@ -491,3 +491,37 @@ def test_forward_mode_through_spawn(cuda):
     _, dts = f.jvp(*args, np.float32(a), wrt=3, tangents=[1.0])
     torch.cuda.synchronize()
     assert np.abs(dts["Q"].cpu().numpy() - dq).max() <= 1e-3 * np.abs(dq).max()
+
+
+def test_forward_mode_through_spawn_lanes_and_limits(cuda):
+    """two tangent lanes through spawn: lane 1 seeded twice lane 0 gives twice the tangent; a max_steps that
+    truncates children poisons value_and_grad's gradient and the float outputs (never a silently partial one)"""
+    from items_lang import spawn_decay
+    args = _decay_args(2000)
+    f = tm.vmap(spawn_decay, outputs={"Q": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=10,
+                spawn=tm.Queue(1 << 16))
+    _, dts = f.jvp(*args, np.float32(1.1), wrt=3, tangents=np.array([[1.0], [2.0]], np.float32))
+    torch.cuda.synchronize()
+    d = dts["Q"].cpu().numpy()
+    assert d.shape == (2, 8) and near(d[1], 2.0 * d[0], 1e-6)
+    ft = tm.vmap(spawn_decay, outputs={"Q": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=2,
+                 spawn=tm.Queue(1 << 16))
+    r, g = ft.value_and_grad(*args, np.float32(1.1), wrt=3, cotangents={"Q": torch.ones(8)})
+    torch.cuda.synchronize()
+    assert int(r.stats["children_truncated"]) > 0 and int(r.stats["n_truncated"]) > 0
+    assert torch.isnan(g).all() and torch.isnan(r.outputs["Q"]).all()
+
+
+def test_traced_shower_value_and_grad(cuda, orc):
+    """the traced shower's value_and_grad w.r.t. X0 runs forward mode through spawn in one launch: X0 moves only the
+    deposit's bin, so the gradient is exactly 0 (as the tree adjoint's); the outputs are the forward's"""
+    E0, d0, keys = orc.sh_inputs(3000)
+    f = _shower_fn()
+    r, g = f.value_and_grad(E0, d0, keys, np.float32(1.0), wrt=3, cotangents={"dep": torch.ones(512)})
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    assert B.run.last["kernel"] == f.last_lowered.vg_program((0,)).kernel
+    assert float(g) == 0.0
+    ref = orc.sh_fwd(E0, d0, keys, 1.0)
+    assert np.array_equal(np_out(r)["count"], ref["count"]) and np.array_equal(r.per_item.cpu().numpy(), ref["k"])
+    assert near(np_out(r)["dep"], ref["dep"])
