@@ -486,7 +486,6 @@ def main():
         n_steps = int(r_last["steps"][0].item())
         n_spawned = int(r_last["stats"][0].item())
         dom = (fused.kernel, 4 * n_steps + 2 * n_spawned, v_ms)
-        cfg.tf = 4
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
     tr = TRAFFIC.get(dom[0])
     traffic = None if tr is None else int(round(tr[0] * N))
@@ -500,7 +499,7 @@ def main():
                          f"over {n_spawned} children; counted by the launch)") if sh_vg else
                         (f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
                          f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
-                         "steps from the per-item trip counts and the replay schedule)")} if cfg.tf else None
+                         "steps from the per-item trip counts and the replay schedule)")} if (cfg.tf or sh_vg) else None
     if roofline is not None and traffic is not None:
         # the memory side of the roofline: the kernel's measured DRAM bytes per launch over its time, against the
         # measured copy bandwidth (MEASURED_PEAKS.json): how far from memory-bound the path is
