@@ -209,11 +209,16 @@ class Mapped:
             order = longest_first(res.per_item)
         return res, self.grad(*moved, wrt=wrt, cotangents=cotangents, order=order)
 
-    def grad(self, *args, wrt, cotangents, order=None):
+    def grad(self, *args, wrt, cotangents, order=None, exact_order=True):
         """d <cotangents, outputs> / d args[wrt] for broadcast operand(s) `wrt` (an argument index or a tuple of
-        them): ONE replay launch.  cotangents: {output name: array of the output's shape}; missing outputs get zero
-        cotangents.  -> a scalar for one index, a vector for a tuple; NaN when an item's replay hit max_steps."""
+        them): ONE replay launch (for the shower: the tree adjoint).  cotangents: {output name: array of the output's
+        shape}; missing outputs get zero cotangents.  -> a scalar for one index, a vector for a tuple; NaN when an
+        item's replay hit max_steps.  exact_order=False: where the family's one-pass program is forward mode (the
+        photon, the shower), that launch instead, its forward outputs discarded -- faster than the replay, which
+        re-runs the forward, and equal to it within the float tolerance."""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        if not exact_order and self.fam.name in ("photon", "shower"):
+            return self.value_and_grad(*args, wrt=wrt, cotangents=cotangents)[1]
         if "tree" in self.fam.grads:
             return self._tree_grad(args, idx, cotangents, wrt)
         if any(self.fam.in_axes[w] is not None for w in idx):

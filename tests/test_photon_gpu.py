@@ -168,3 +168,17 @@ def test_ph_api_value_and_grad_onepass(cuda):
     assert near(g1.cpu().numpy(), g2.cpu().numpy())
     assert np.array_equal(r1.per_item.cpu().numpy(), r2.per_item.cpu().numpy())
     assert near(r1.outputs["dep"].cpu().numpy(), r2.outputs["dep"].cpu().numpy())
+
+
+def test_ph_api_grad_forward_mode_option(cuda):
+    """grad(exact_order=False) runs the forward-mode launch; within the float tolerance of the replay's"""
+    import tallymap_b200 as tm
+    keys = prng.split(prng.PRNGKey(5), 100000)
+    f = tm.vmap("photon", outputs={"dep": tm.Sum((64, 64, 64))}, in_axes=(0, None, None))
+    cts = {"dep": torch.ones((64, 64, 64))}
+    g1 = f.grad(keys, np.float32(0.1), np.float32(10.0), wrt=(1, 2), cotangents=cts, exact_order=False)
+    assert B.run.last["kernel"] == "ph_vg_onepass"
+    g2 = f.grad(keys, np.float32(0.1), np.float32(10.0), wrt=(1, 2), cotangents=cts)
+    assert B.run.last["kernel"] == "ph_grad"
+    torch.cuda.synchronize()
+    assert near(g1.cpu().numpy(), g2.cpu().numpy())
