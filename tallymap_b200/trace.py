@@ -457,7 +457,9 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
         _CTX.pop()
     st = tr.loop_state
     if not st.get("done"):
-        raise TraceError("tallymap_b200.lang: the item has no while_loop (the step schedule needs one)")
+        # no loop: a loop of zero steps (its predicate false), all the item's code after it
+        st.update(done=True, init=[], carry=[], cond=[], cond_out=Lit(False, BOOL), body=[], body_out=[],
+                  post_carry=[], pre_len=0)
     out = out if isinstance(out, tuple) else (out,)
     if not out or not isinstance(out[0], TallyToken):
         raise TraceError("tallymap_b200.lang: an item returns (t, *per_item_results)")

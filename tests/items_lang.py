@@ -129,3 +129,12 @@ def spawn_decay(t, g, w, key, a):
     k, w, t = tl.while_loop(lambda c: c[0] < 3, body, (0, w, t))
     t = t.spawn((g + 1, w * a, tl.random.fold_in(key, 7)), when=g < 2)
     return t, k
+
+
+def scatter(t, x, key, a):
+    """a loop-free item (no while_loop: the reference's 'item' schedule; here a loop of zero steps): two draws, two
+    emits, a per-item result"""
+    u, v = tl.random.uniform(key, (2,))
+    t = t.add("h", ((x + u) * 4).astype(tl.int32), a * x * v)
+    t = t.add("s", 0, tl.exp(-a * u))
+    return t, x * 2 + u

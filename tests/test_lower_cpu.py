@@ -55,10 +55,10 @@ def test_trace_errors():
     with pytest.raises(T.TraceError, match="one top-level"):
         T.trace_item(two_loops, ["f32", "key", "f32"], 2, {})
 
-    def no_loop(t, x, key, d):
+    def no_loop(t, x, key, d):        # (a loop-free item: a loop of zero steps, its code after it)
         return t, x
-    with pytest.raises(T.TraceError, match="no while_loop"):
-        T.trace_item(no_loop, ["f32", "key", "f32"], 2, {})
+    tr0 = T.trace_item(no_loop, ["f32", "key", "f32"], 2, {})
+    assert tr0.carry == [] and tr0.body == [] and not tr0.cond_out.value
 
     def mixed(t, x, key, d):
         def body(c):
@@ -249,3 +249,16 @@ def test_forward_mode_through_spawn_lowers():
     assert "float d1_0;" in src and "start_child(Ctx& c, const Child& ch)" in src and "spawn_body<tmb::GenJvp>" in src
     j = L.jvp_program((0,), 2)
     assert j.spawns and j.queue_leaf_bytes == 4 * (4 + 2)
+
+
+def test_loop_free_item_lowers_and_evaluates(orc):
+    """a loop-free item lowers (forward, one-pass value-and-grad, replay) and the evaluator runs it"""
+    from items_lang import scatter
+    from oracle.ir_eval import Evaluator
+    f = tm.vmap(scatter, outputs={"h": tm.Sum((8,)), "s": tm.Sum(())}, in_axes=(0, 0, None))
+    args = _args_walk(32)
+    L = f.lowered(args)
+    assert L.vg_program((0,)) is not None and L.grad_program((0,)).replay_state_bytes == 4
+    tr = T.trace_item(scatter, ["f32", "key", "f32"], 2, {"h": ((8,), "f32"), "s": ((), "f32")})
+    r = Evaluator(tr, 100).run(list(args[:2]), [1.0])
+    assert not r["trunc"].any() and r["sums"]["s"][0] > 0

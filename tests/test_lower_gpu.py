@@ -525,3 +525,31 @@ def test_traced_shower_value_and_grad(cuda, orc):
     ref = orc.sh_fwd(E0, d0, keys, 1.0)
     assert np.array_equal(np_out(r)["count"], ref["count"]) and np.array_equal(r.per_item.cpu().numpy(), ref["k"])
     assert near(np_out(r)["dep"], ref["dep"])
+
+
+def test_loop_free_item(cuda):
+    """an item with no loop (a zero-step loop): outputs and per-item results against the IR evaluator, the one-pass
+    gradient against the replay's and a central difference of the evaluator"""
+    from items_lang import scatter
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    x, k = rw_inputs(20000, seed=21)
+    a = 0.7
+    f = tm.vmap(scatter, outputs={"h": tm.Sum((8,)), "s": tm.Sum(())}, in_axes=(0, 0, None))
+    r = f(x, k, np.float32(a))
+    torch.cuda.synchronize()
+    tr = T.trace_item(scatter, ["f32", "key", "f32"], 2, {"h": ((8,), "f32"), "s": ((), "f32")})
+    ev = lambda av: Evaluator(tr, 2 ** 31 - 1).run([x, k], [np.float32(av)])
+    ref = ev(a)
+    assert np.array_equal(bits(r.per_item.cpu().numpy()), bits(ref["results"][0]))
+    assert near(np_out(r)["h"], ref["sums"]["h"]) and near(np_out(r)["s"], ref["sums"]["s"])
+    cts = {"h": torch.linspace(-1, 1, 8), "s": torch.full((), 2.0)}
+    r1, g1 = f.value_and_grad(x, k, np.float32(a), wrt=2, cotangents=cts)
+    r2, g2 = f.value_and_grad(x, k, np.float32(a), wrt=2, cotangents=cts, exact_order=True)
+    torch.cuda.synchronize()
+    assert near(g1.cpu().numpy(), g2.cpu().numpy())
+    h = 1e-3
+    ct = np.linspace(-1, 1, 8)
+    fd = lambda av: float(np.dot(ct, ev(av)["sums"]["h"]) + 2.0 * ev(av)["sums"]["s"][0])
+    want = (fd(a + h) - fd(a - h)) / (2 * h)
+    assert abs(float(g2) - want) <= 2e-3 * abs(want)
