@@ -1,7 +1,8 @@
 """The operations an item function may use, for tracing (tallymap_b200.trace): a scalar subset of jax.numpy,
 jax.random and lax.while_loop with jax's semantics, the ones the reference's op table lowers for these items
 (tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
-random_bits / fold_in / split, while).
+random_bits / fold_in / split, while), and compositions of them with jax's semantics (clip, sign, square,
+random.bernoulli).
 
     from tallymap_b200 import lang as tl
 
@@ -96,6 +97,24 @@ def where(c, a, b):
     return T._cur().emit("select", [c, a, b], [a.dtype])[0]
 
 
+def clip(x, a_min, a_max):
+    """jnp.clip: maximum(a_min, x), then minimum(a_max, .) (lax.max / min semantics: NaN propagates)"""
+    return minimum(a_max, maximum(a_min, x))
+
+
+def sign(x):
+    """jnp.sign (lax.sign): -1, +1, the zero itself for +-0 (its sign kept), NaN for NaN"""
+    x = T._lit(x)
+    if x.dtype == T.F32:
+        return where(x > 0.0, 1.0, where(x < 0.0, -1.0, x))
+    return where(x > 0, 1, where(x < 0, -1, 0))
+
+
+def square(x):
+    """jnp.square: x * x"""
+    return x * x
+
+
 class random:
     """jax.random on raw uint32[2] key data, partitionable threefry (bitwise jax.random's)"""
 
@@ -125,6 +144,12 @@ class random:
         n = _count(shape)
         out = tuple(T._cur().emit("bits", [key.a, key.b, T.Lit(i, T.U32)], [T.U32])[0] for i in range(n))
         return out[0] if shape == () else out
+
+    @staticmethod
+    def bernoulli(key, p=0.5, shape=()):
+        """jax.random.bernoulli: uniform(key, shape) < p"""
+        u = random.uniform(key, shape)
+        return tuple(v < p for v in u) if isinstance(u, tuple) else u < p
 
     @staticmethod
     def uniform(key, shape=(), dtype=float32, minval=0.0, maxval=1.0):

@@ -138,3 +138,19 @@ def scatter(t, x, key, a):
     t = t.add("h", ((x + u) * 4).astype(tl.int32), a * x * v)
     t = t.add("s", 0, tl.exp(-a * u))
     return t, x * 2 + u
+
+
+def extras(t, a, key, n, s):
+    """the compositions of lowered primitives (clip, sign, square, bernoulli) on awkward values, recorded so that they
+    compare bitwise"""
+    def body(c):
+        k, x, t = c
+        kk = tl.random.fold_in(key, k)
+        u = tl.random.uniform(kk)
+        hit = tl.random.bernoulli(kk, 0.3)
+        y = tl.clip(x * s, -2.0, 3.0)
+        z = tl.sign(x) * tl.square(u - 0.5) + tl.sign(tl.floor(x * 0.5)).astype(tl.float32)
+        t = t.append("rec", {"y": y, "z": z, "h": hit.astype(tl.int32), "g": tl.sign((x * 3.0).astype(tl.int32))})
+        return k + 1, x * (1.5 - u) - 0.25, t
+    k, x, t = tl.while_loop(lambda c: c[0] < n, body, (0, a, t))
+    return t, k

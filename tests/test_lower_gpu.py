@@ -553,3 +553,30 @@ def test_loop_free_item(cuda):
     fd = lambda av: float(np.dot(ct, ev(av)["sums"]["h"]) + 2.0 * ev(av)["sums"]["s"][0])
     want = (fd(a + h) - fd(a - h)) / (2 * h)
     assert abs(float(g2) - want) <= 2e-3 * abs(want)
+
+
+def test_lowered_compositions_against_ir_evaluator(cuda):
+    """clip, sign, square and bernoulli on awkward values (NaN, +-inf, +-0, huge), bitwise through Records"""
+    from items_lang import extras
+    vals = np.float32([np.nan, np.inf, -np.inf, -0.0, 0.0, 1e38, -1e38, 3e-39, -7.5, 7.5, 0.6, 123456.0, -2.0, 0.25])
+    n = len(vals)
+    keys = prng.split(prng.PRNGKey(23), n)
+    args = (vals, keys, np.full(n, 4, np.int32), np.float32(0.7))
+    fields = {"y": torch.float32, "z": torch.float32, "h": torch.int32, "g": torch.int32}
+    f = tm.vmap(extras, outputs={"rec": tm.Records(fields, capacity=128)}, in_axes=(0, 0, 0, None), max_steps=10)
+    r = f(*args)
+    torch.cuda.synchronize()
+    recspec = {"rec": (128, tuple((k, "f32" if v == torch.float32 else "i32") for k, v in sorted(fields.items())))}
+    ref = _eval(extras, ["f32", "key", "i32", "f32"], 3, {}, recspec, args, 10)
+    m = len(ref["records"]["rec"])
+    assert m == 4 * n and int(r.stats["appended"]["rec"]) == m
+    got = {k: v.cpu().numpy() for k, v in r.outputs["rec"].items()}
+    for j, (fname, _) in enumerate(recspec["rec"][1]):
+        want = np.array([rec[j] for rec in ref["records"]["rec"]])
+        g = got[fname][:m]
+        if g.dtype == np.float32:
+            w = want.astype(np.float32)
+            same = (g.view(np.uint32) == w.view(np.uint32)) | (np.isnan(g) & np.isnan(w))
+            assert same.all(), fname
+        else:
+            assert np.array_equal(g.astype(np.int64), want.astype(np.int64)), fname
