@@ -428,15 +428,17 @@ class MappedFn:
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
     def grad(self, *args, wrt, cotangents, order=None):
-        """d <cotangents, outputs> / d args[wrt] for float32 broadcast operand(s) `wrt`: ONE replay launch of the
-        generated adjoint.  -> a scalar for one index, a vector for a tuple; NaN when an item's replay hit
-        max_steps."""
+        """d <cotangents, outputs> / d args[wrt] for float32 operand(s) `wrt`: ONE replay launch of the generated
+        adjoint.  A broadcast operand's cotangent is summed over the items (exactly); a per-item operand's is per
+        item (shape (N,) or (N, n)).  -> one cotangent for one index, a tuple in `wrt`'s order for a tuple (for
+        broadcast operands only: a vector, as before); NaN when an item's replay hit max_steps."""
         L = self.lowered(args)
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
-        if any(self.in_axes[w] is not None for w in idx):
-            raise ValueError("tallymap_b200: grad with respect to a per-item operand is not lowered")
-        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
-        prog = L.grad_program(bpos)
+        bidx = [w for w in idx if self.in_axes[w] is None]
+        pidx = [w for w in idx if self.in_axes[w] == 0]
+        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in bidx)
+        ppos = tuple(sum(1 for ax in self.in_axes[:w] if ax == 0) for w in pidx)
+        prog = L.grad_program(bpos, ppos)
         pi, bc = self._split(args)
         n = int((pi[0] if isinstance(pi[0], torch.Tensor) else B._host(pi[0])).shape[0]) if pi else 0
         cts = []
@@ -447,9 +449,15 @@ class MappedFn:
             cts.append(torch.zeros(shape, dtype=torch.float32) if c is None else c)
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
         ct = out[0].reshape(-1)
-        trunc = out[2]
-        ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
-        return ct.reshape(()) if isinstance(wrt, int) else ct
+        ys = out[2:]
+        bad = ys[prog.trunc].bool().any()
+        nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
+        if not pidx:
+            ct = nan(ct)
+            return ct.reshape(()) if isinstance(wrt, int) else ct
+        got = {w: nan(ct[q]).reshape(()) for q, w in enumerate(bidx)}
+        got.update({w: nan(ys[q]) for q, w in enumerate(pidx)})
+        return got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx)
 
     def jvp(self, *args, wrt, tangents):
         """forward mode (tallymap's jvp of a mapped call, _api.py:305-345): ONE launch of the generated tangent program.

@@ -678,12 +678,23 @@ class _Rev:
             raise LowerError(f"tallymap_b200.lower: no reverse rule for {p}")
 
 
-def grad_source(it, wrt, standalone=True):
+def grad_source(it, wrt, standalone=True, wrt_pi=()):
     """-> (C source of the replay ITEM for d <ct, outputs> / d bc[wrt], stored-state bytes, shared-memory bytes);
-    standalone=False: the ITEM struct alone, its State the forward ITEM's (GenFwd: for the one-pass program)"""
+    standalone=False: the ITEM struct alone, its State the forward ITEM's (GenFwd: for the one-pass program).
+    wrt_pi: per-item operands (positions among them, float32 scalars or vectors) whose per-item cotangents the
+    program also writes (the reference's perturbed per-item inputs, _reverse.py vjp_prog `ip`): per-item results
+    f32[N] (or f32[N, n]) before the truncation flag."""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
-    act, carry_act = _active(it, wrt)
+    pl = []                               # (output q, the per-item operand's leaves)
+    for j in wrt_pi:
+        x = it.pi[j]
+        leaves = list(x) if isinstance(x, tuple) else [x]
+        if isinstance(x, T.Key) or any(v.dtype != T.F32 for v in leaves):
+            raise LowerError("tallymap_b200.lower: only float32 per-item operands are differentiable")
+        pl.append(leaves)
+    act, carry_act = _active(it, wrt, extra=[v.id for leaves in pl for v in leaves])
+    Wx = max(W, 1)                        # (one unused bin when only per-item operands are differentiated)
     ftal = [(t, name, shape) for t, (name, (shape, dt)) in enumerate(it.specs) if dt == T.F32]
     lines = [PRELUDE, "namespace tmb {", "struct GenGrad {"]
     idx = 0
@@ -694,13 +705,17 @@ def grad_source(it, wrt, standalone=True):
         enum.append(f"kBc{k} = {idx}"); idx += 1
     for q, (t, name, shape) in enumerate(ftal):
         enum.append(f"kCt{q} = {idx}"); idx += 1
-    for nm in ("kConsts", "kOrder", "kG", "kExact", "kCtl", "kStats", "kTrunc", "kReplay"):
+    for nm in ("kConsts", "kOrder", "kG", "kExact", "kCtl", "kStats"):
+        enum.append(f"{nm} = {idx}"); idx += 1
+    for q in range(len(pl)):
+        enum.append(f"kGpi{q} = {idx}"); idx += 1
+    for nm in ("kTrunc", "kReplay"):
         enum.append(f"{nm} = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
     lines.append("  enum { kConstM = 0, kConstC = 1, kConstThreads = 2 };")
     # output cotangents: staged in shared memory when small
-    smem = f"ExactBins<{W}>::kSmemBytes"
+    smem = f"ExactBins<{Wx}>::kSmemBytes"
     off = 0
     ct_tally = {}
     stage_lines = []
@@ -710,7 +725,7 @@ def grad_source(it, wrt, standalone=True):
         if S * 4 <= PRIV_BYTES:
             ctx_ct.append(f"    const float* ct{q};")
             stage_lines.append(f"    {{ const float* src = static_cast<const float*>(P.p[kCt{q}]); "
-                               f"float* d = reinterpret_cast<float*>(smem + ExactBins<{W}>::kSmemBytes + {off}); "
+                               f"float* d = reinterpret_cast<float*>(smem + ExactBins<{Wx}>::kSmemBytes + {off}); "
                                f"for (int b = threadIdx.x; b < {S}; b += blockDim.x) d[b] = __ldg(&src[b]); }}")
             ct_tally[name] = (f"c.ct{q}", S, off)
             off += S * 4
@@ -719,17 +734,18 @@ def grad_source(it, wrt, standalone=True):
             ct_tally[name] = (f"c.ct{q}", S, None)
     lines.append(f"  static constexpr int kSmemBytes = {smem} + {off};")
     # (ExactBins<W>::kSmemBytes -- block words, flags, the threads' private words -- and the staged cotangents)
-    smem_bytes = W * 5 * 8 + ((W * 4 + 7) // 8) * 8 + W * 5 * 8 * 128 + off
+    smem_bytes = Wx * 5 * 8 + ((Wx * 4 + 7) // 8) * 8 + Wx * 5 * 8 * 128 + off
     ctx = ["  struct Ctx {"]
     for j, s in enumerate(it.in_specs[:npi]):
         ctx.append(f"    const {_in_ctype(s)}* in{j};")
     for k, b in enumerate(it.bc):
         ctx.append(f"    {CTYPE[b.dtype]} b{k};")
     ctx += ["    i32 M;", "    i32* stats;", "    u64* gw;", "    float* g;", "    uint8_t* trunc;"]
+    ctx += [f"    float* gpi{q};" for q in range(len(pl))]
     ctx += ctx_ct
     for i in it.saved:
         ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
-    ctx.append(f"    mutable ExactPrivS<{W}> pv;")
+    ctx.append(f"    mutable ExactPrivS<{Wx}> pv;")
     ctx.append("  };")
     lines += ctx
     if standalone:
@@ -769,13 +785,14 @@ def grad_source(it, wrt, standalone=True):
     lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
     lines += ["    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.gw = static_cast<u64*>(P.p[kExact]);",
               "    c.g = static_cast<float*>(P.p[kG]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
+    lines += [f"    c.gpi{q} = static_cast<float*>(P.p[kGpi{q}]);" for q in range(len(pl))]
     for q, (t, name, shape) in enumerate(ftal):
         ptr, S, o = ct_tally[name]
         if o is not None:
-            lines.append(f"    c.ct{q} = reinterpret_cast<const float*>(smem + ExactBins<{W}>::kSmemBytes + {o});")
+            lines.append(f"    c.ct{q} = reinterpret_cast<const float*>(smem + ExactBins<{Wx}>::kSmemBytes + {o});")
         else:
             lines.append(f"    c.ct{q} = static_cast<const float*>(P.p[kCt{q}]);")
-    lines.append(f"    c.pv.bind(smem + ExactBins<{W}>::kPrivOffset);")
+    lines.append(f"    c.pv.bind(smem + ExactBins<{Wx}>::kPrivOffset);")
     lines.append("  }")
     lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
     lines += stage_lines
@@ -886,13 +903,17 @@ def grad_source(it, wrt, standalone=True):
         if bid in rev.ct:
             tot = f"({tot} + {rev.ct[bid]})"
         lines.append(f"    if (c.pv.emit({q}, {tot})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
+    for q, leaves in enumerate(pl):
+        # the per-item operand's cotangent: what the pre-loop VJP gathered into its leaves (+0 for an unused one)
+        for e_, v in enumerate(leaves):
+            lines.append(f"    c.gpi{q}[item * {len(leaves)} + {e_}] = {rev.ct.get(v.id, '0.0f')};")
     lines.append("    c.trunc[item] = (fin.kc >= c.M && pred(c, fin)) ? 1 : 0;")
     lines.append("  }")
     lines.append("  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {")
-    lines.append(f"    ExactBins<{W}>::flush(c.pv, smem, c.gw, c.stats, tid);")
+    lines.append(f"    ExactBins<{Wx}>::flush(c.pv, smem, c.gw, c.stats, tid);")
     lines.append("  }")
     lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int) {")
-    lines.append(f"    if (tid == 0) ExactBins<{W}>::readout(c.gw, c.g, c.stats);")
+    lines.append(f"    if (tid == 0) ExactBins<{Wx}>::readout(c.gw, c.g, c.stats);")
     lines.append("  }")
     lines.append("};")
     if not standalone:
@@ -1073,32 +1094,37 @@ class Lowered:
             self.vgs[wrt] = prog
         return self.vgs[wrt]
 
-    def grad_program(self, wrt):
-        """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands)"""
+    def grad_program(self, wrt, wrt_pi=()):
+        """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands) and, per
+        item, d <ct, outputs> / d pi[wrt_pi] (positions among the per-item operands: per-item results before the
+        truncation flag)"""
         from .backend import ItemProgram, TSpec
-        wrt = tuple(wrt)
+        wrt, wrt_pi = tuple(wrt), tuple(wrt_pi)
         if self.fwd.records:
             raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
         if self.it.spawns:
             raise NotImplementedError("tallymap_b200: reverse mode through spawn (the tree adjoint) is lowered for "
                                       "the built-in shower only")
-        if wrt not in self.grads:
+        key = wrt if not wrt_pi else (wrt, wrt_pi)
+        if key not in self.grads:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:
                     raise LowerError("tallymap_b200.lower: only float32 broadcast operands are differentiable")
-            src, stored, smem = grad_source(self.it, list(wrt))
+            src, stored, smem = grad_source(self.it, list(wrt), wrt_pi=wrt_pi)
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             from .backend import Operand
             bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
-            nbuf = len(self.pi) + len(bc) + 2 + 4 + 2
-            kid = compile_kernel(src, f"{self.name}_grad{''.join(map(str, wrt))}", nbuf, smem)
-            self.grads[wrt] = ItemProgram(f"{self.name}_grad", kid, pi=self.pi, bc=bc,
+            ys = tuple(Operand(f"ct_in{j}", self.pi[j].shape, torch.float32) for j in wrt_pi)
+            ys += (_operand("truncated", T.BOOL),)
+            nbuf = len(self.pi) + len(bc) + 2 + 4 + len(ys) + 1
+            tag = "".join(map(str, wrt)) + ("_pi" + "".join(map(str, wrt_pi)) if wrt_pi else "")
+            kid = compile_kernel(src, f"{self.name}_grad{tag}", nbuf, smem)
+            self.grads[key] = ItemProgram(f"{self.name}_grad", kid, pi=self.pi, bc=bc,
                                           consts=("max_steps", "rev_checkpoints", "replay_threads"),
-                                          tallies=(TSpec("ct", (len(wrt),), exact=True),),
-                                          ys=(_operand("truncated", T.BOOL),), trunc=0,
+                                          tallies=(TSpec("ct", (max(len(wrt), 1),), exact=True),),
+                                          ys=ys, trunc=len(ys) - 1,
                                           replay_state_bytes=(stored + 3) // 4 * 4)
-        return self.grads[wrt]
-
+        return self.grads[key]
 
 
 # ------------------------------------------------------------------------------------------------ forward mode

@@ -154,3 +154,16 @@ def extras(t, a, key, n, s):
         return k + 1, x * (1.5 - u) - 0.25, t
     k, x, t = tl.while_loop(lambda c: c[0] < n, body, (0, a, t))
     return t, k
+
+
+def affine(t, x, key, a):
+    """n = 6 steps of x <- x * a + u, emitting x^2 at bin k % 8: smooth in the per-item x and the broadcast a, so its
+    per-item gradient has a closed form (d x_k / d x_0 = a^k)"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        x = x * a + u
+        t = t.add("h", k % 8, x * x)
+        return k + 1, x, t
+    k, x, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
+    return t, x

@@ -262,3 +262,16 @@ def test_loop_free_item_lowers_and_evaluates(orc):
     tr = T.trace_item(scatter, ["f32", "key", "f32"], 2, {"h": ((8,), "f32"), "s": ((), "f32")})
     r = Evaluator(tr, 100).run(list(args[:2]), [1.0])
     assert not r["trunc"].any() and r["sums"]["s"][0] > 0
+
+
+def test_per_item_operand_gradient_program():
+    """grad w.r.t. a per-item operand: the generated replay writes each item's cotangent before the flag"""
+    from items_lang import affine
+    f = tm.vmap(affine, outputs={"h": tm.Sum((8,))}, in_axes=(0, 0, None), max_steps=10)
+    L = f.lowered(_args_walk(16))
+    p = L.grad_program((0,), (0,))
+    assert [y.name for y in p.ys] == ["ct_in0", "truncated"] and p.trunc == 1
+    p0 = L.grad_program((), (0,))
+    assert p0.tallies[0].shape == (1,)
+    src = lower.grad_source(L.it, [0], wrt_pi=(0,))[0]
+    assert "c.gpi0[item * 1 + 0] =" in src

@@ -580,3 +580,35 @@ def test_lowered_compositions_against_ir_evaluator(cuda):
             assert same.all(), fname
         else:
             assert np.array_equal(g.astype(np.int64), want.astype(np.int64)), fname
+
+
+def test_per_item_operand_gradient(cuda):
+    """grad w.r.t. a per-item operand (each item's own cotangent) and the broadcast one in one replay launch,
+    against the closed form of an affine recursion (d x_k / d x_0 = a^k) in float64"""
+    from items_lang import affine
+    n, a = 20000, np.float32(0.9)
+    x, k = rw_inputs(n, seed=31)
+    ct = np.linspace(-1.0, 1.0, 8).astype(np.float32)
+    f = tm.vmap(affine, outputs={"h": tm.Sum((8,))}, in_axes=(0, 0, None), max_steps=10)
+    gx, ga = f.grad(x, k, a, wrt=(0, 2), cotangents={"h": torch.from_numpy(ct)})
+    gx1 = f.grad(x, k, a, wrt=0, cotangents={"h": torch.from_numpy(ct)})
+    torch.cuda.synchronize()
+    assert gx.shape == (n,) and np.array_equal(bits(gx.cpu().numpy()), bits(gx1.cpu().numpy()))
+    # the closed form in float64 (the draws exactly as the item's)
+    xs = x.astype(np.float64)
+    dxdx0 = np.ones(n)
+    dxda = np.zeros(n)
+    want_x = np.zeros(n)
+    want_a = 0.0
+    for s in range(6):
+        kk = prng.fold_in(k, s)
+        o0, o1 = prng.threefry2x32(kk[:, 0], kk[:, 1], np.uint32(0), np.uint32(0))
+        u = (((o0 ^ o1) >> np.uint32(9)) | np.uint32(0x3F800000)).view(np.float32) - np.float32(1.0)
+        dxda = xs + float(a) * dxda
+        dxdx0 = float(a) * dxdx0
+        xs = xs * float(a) + u.astype(np.float64)
+        want_x += float(ct[s % 8]) * 2.0 * xs * dxdx0
+        want_a += float((float(ct[s % 8]) * 2.0 * xs * dxda).sum())
+    g = gx.cpu().numpy().astype(np.float64)
+    assert np.abs(g - want_x).max() <= 1e-4 * np.abs(want_x).max()
+    assert abs(float(ga) - want_a) <= 1e-4 * abs(want_a)
