@@ -500,6 +500,13 @@ def main():
                         (f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
                          f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
                          "steps from the per-item trip counts and the replay schedule)")} if (cfg.tf or sh_vg) else None
+    if roofline is not None and not tree:
+        # per mode (the separate launches): the forward and the replay gradient against the same probe
+        roofline["modes"] = {
+            "fwd": {"kernel": cfg.fwd.kernel, "achieved": round(tf_fwd / (f_ms / 1e3) / 1e9, 2),
+                    "frac": round(tf_fwd / (f_ms / 1e3) / 1e9 / peak, 4)},
+            "grad": {"kernel": cfg.grad.kernel, "achieved": round(tf_grad / (g_ms / 1e3) / 1e9, 2),
+                     "frac": round(tf_grad / (g_ms / 1e3) / 1e9 / peak, 4)}}
     if roofline is not None and traffic is not None:
         # the memory side of the roofline: the kernel's measured DRAM bytes per launch over its time, against the
         # measured copy bandwidth (MEASURED_PEAKS.json): how far from memory-bound the path is
