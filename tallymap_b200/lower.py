@@ -15,7 +15,6 @@ Launch layouts are the backend's (backend.ItemProgram): forward = [per-item][bro
 i32[3]][order] | [g f32[W]][exact words][ctl][stats] | [truncated][replay scratch].
 """
 import ctypes
-import dataclasses
 import hashlib
 import os
 
@@ -1037,16 +1036,17 @@ class Lowered:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:
                     raise LowerError("tallymap_b200.lower: only float32 broadcast operands have tangents")
-            if self.it.exact or self.fwd.records:
-                raise NotImplementedError("tallymap_b200: forward mode of fixed_point or Records outputs is not "
-                                          "lowered")
+            if self.fwd.records:
+                raise NotImplementedError("tallymap_b200: forward mode of Records outputs is not lowered")
             src, smem = jvp_source(self.it, list(wrt), int(lanes))
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
-            tallies = self.fwd.tallies + tuple(TSpec("d_" + nm, (int(lanes),) + tuple(shape)) for nm, shape in fts)
-            tallies = tuple(dataclasses.replace(t, exact=False) for t in tallies)
+            # a fixed-point output's tangent is exact too (the same accumulator)
+            tallies = self.fwd.tallies + tuple(TSpec("d_" + nm, (int(lanes),) + tuple(shape), exact=nm in self.it.exact)
+                                               for nm, shape in fts)
             sp = self.it.spawns
-            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 2 + len(self.fwd.ys) + (3 if sp else 0)
+            nx = sum(1 for t in tallies if t.exact)
+            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + 2 + len(self.fwd.ys) + (3 if sp else 0)
             kid = compile_kernel(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
             self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc,
                                          consts=("max_steps", "queue") if sp else ("max_steps",),
@@ -1079,10 +1079,11 @@ class Lowered:
                 if not sp and not has_active_carry(self.it, list(wrt)):
                     src, smem, nbuf = onepass_source(self.it, list(wrt))
                     kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
-                elif len(wrt) <= FWD_GRAD_MAX and not self.it.exact:
+                elif len(wrt) <= FWD_GRAD_MAX:
                     # forward mode; through spawn, each child carries its float leaves' tangents
                     src, smem = jvp_source(self.it, list(wrt), len(wrt), contract=True)
-                    nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + 1 + 2 + len(self.fwd.ys) + (3 if sp else 0)
+                    nx = sum(1 for t in tallies if t.exact)
+                    nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + 2 + len(self.fwd.ys) + (3 if sp else 0)
                     kid = compile_kernel(src, f"{self.name}_fg{''.join(map(str, wrt))}", nbuf, smem)
                 else:
                     kid = None
@@ -1256,12 +1257,21 @@ def jvp_source(it, wrt, L, contract=False):
     enum.append(f"kOrder = {idx}"); idx += 1
     for t, _ in enumerate(it.specs):
         enum.append(f"kT{t} = {idx}"); idx += 1
+    # fixed-point outputs (Sum(fixed_point=True)): exact words after every tally (the primal's, then -- forward
+    # mode proper -- their tangents', which use the same exact accumulator: the reference's same-scale tangent)
+    ex = [(t, name) for t, (name, _) in enumerate(it.specs) if name in it.exact]
     if contract:
         enum.append(f"kG = {idx}"); idx += 1
+        for t, _ in ex:
+            enum.append(f"kX{t} = {idx}"); idx += 1
         enum.append(f"kExact = {idx}"); idx += 1
     else:
         for q, _ in enumerate(ftal):
             enum.append(f"kD{q} = {idx}"); idx += 1
+        for t, _ in ex:
+            enum.append(f"kX{t} = {idx}"); idx += 1
+        for t, _ in ex:
+            enum.append(f"kDX{t} = {idx}"); idx += 1
     if sp:
         enum.append(f"kSeq = {idx}"); idx += 1
         enum.append(f"kQctl = {idx}"); idx += 1
@@ -1292,14 +1302,16 @@ def jvp_source(it, wrt, L, contract=False):
                 smem += (S * 4 + 15) // 16 * 16
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
-        if S * 4 <= PRIV_BYTES:
+        nb = S * 44 if name in it.exact else S * 4
+        if nb <= (4 * PRIV_BYTES if name in it.exact else PRIV_BYTES):
             priv[("p", name)] = smem
-            smem += (S * 4 + 15) // 16 * 16
+            smem += (nb + 15) // 16 * 16
     for q, (t, name, shape) in enumerate(ftal):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
-        if not contract and L * S * 4 <= PRIV_BYTES:
+        nb = L * S * 44 if name in it.exact else L * S * 4
+        if not contract and nb <= (4 * PRIV_BYTES if name in it.exact else PRIV_BYTES):
             priv[("d", name)] = smem
-            smem += (L * S * 4 + 15) // 16 * 16
+            smem += (nb + 15) // 16 * 16
     lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
     ctx = ["  struct Ctx {"]
     for j, s in enumerate(it.in_specs[:npi]):
@@ -1316,14 +1328,22 @@ def jvp_source(it, wrt, L, contract=False):
         sizes[name] = S
         ct = "float" if dt == T.F32 else "i32"
         ctx.append(f"    {ct}* g{t};")
-        if ("p", name) in priv:
+        if name in it.exact:
+            ctx.append(f"    u64* x{t};")
+            if ("p", name) in priv:
+                ctx.append(f"    u64* sx{t};")
+            if not contract:
+                ctx.append(f"    u64* dx{t};")
+                if ("d", name) in priv:
+                    ctx.append(f"    u64* sdx{t};")
+        elif ("p", name) in priv:
             ctx.append(f"    {ct}* s{t};")
     for q, (t, name, shape) in enumerate(ftal):
         if contract:
             ctx.append(f"    const float* ct{t};")
             continue
         ctx.append(f"    float* gd{t};")
-        if ("d", name) in priv:
+        if ("d", name) in priv and name not in it.exact:
             ctx.append(f"    float* sd{t};")
     if contract:
         ctx += ["    u64* gw;", "    float* g;", f"    mutable ExactPrivS<{W}> pv;"]
@@ -1365,7 +1385,15 @@ def jvp_source(it, wrt, L, contract=False):
     for t, (name, (shape, dt)) in enumerate(it.specs):
         ct = "float" if dt == T.F32 else "i32"
         lines.append(f"    c.g{t} = static_cast<{ct}*>(P.p[kT{t}]);")
-        if ("p", name) in priv:
+        if name in it.exact:
+            lines.append(f"    c.x{t} = static_cast<u64*>(P.p[kX{t}]);")
+            if ("p", name) in priv:
+                lines.append(f"    c.sx{t} = reinterpret_cast<u64*>(smem + {priv[('p', name)]});")
+            if not contract:
+                lines.append(f"    c.dx{t} = static_cast<u64*>(P.p[kDX{t}]);")
+                if ("d", name) in priv:
+                    lines.append(f"    c.sdx{t} = reinterpret_cast<u64*>(smem + {priv[('d', name)]});")
+        elif ("p", name) in priv:
             lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[('p', name)]});")
     for q, (t, name, shape) in enumerate(ftal):
         if contract:
@@ -1375,7 +1403,7 @@ def jvp_source(it, wrt, L, contract=False):
                 lines.append(f"    c.ct{t} = static_cast<const float*>(P.p[kCt{q}]);")
             continue
         lines.append(f"    c.gd{t} = static_cast<float*>(P.p[kD{q}]);")
-        if ("d", name) in priv:
+        if ("d", name) in priv and name not in it.exact:
             lines.append(f"    c.sd{t} = reinterpret_cast<float*>(smem + {priv[('d', name)]});")
     if contract:
         lines += ["    c.gw = static_cast<u64*>(P.p[kExact]);", "    c.g = static_cast<float*>(P.p[kG]);",
@@ -1399,6 +1427,8 @@ def jvp_source(it, wrt, L, contract=False):
     def emitter(name, idx_c, v_c):
         t, S, dt = tidx[name], sizes[name], it.tr.specs[name][1]
         pv = ("p", name) in priv
+        if name in it.exact:
+            return f"ExactSum<{S}>::emit({'c.sx' if pv else 'c.x'}{t}, c.stats, {idx_c}, {v_c});"
         if dt == T.F32:
             if pv:
                 return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
@@ -1414,6 +1444,10 @@ def jvp_source(it, wrt, L, contract=False):
             # the tangent emit contracted with the cotangent at its index (an out-of-range index adds nothing)
             a_ = f"{acc['p']}{l}"
             return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) {a_} = {a_} + c.ct{t}[b_] * {dv_c}; }}"
+        if name in it.exact:
+            w_ = f"c.sdx{t}" if ("d", name) in priv else f"c.dx{t}"
+            return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) ExactSum<{L * S}>::emit({w_}, c.stats, "
+                    f"{l * S} + b_, {dv_c}); }}")
         tgt = f"c.sd{t}" if ("d", name) in priv else f"c.gd{t}"
         # (an out-of-range index is counted once, by the primal emit)
         return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) fatom(&{tgt}[{l * S} + b_], {dv_c}); }}"
@@ -1526,21 +1560,29 @@ def jvp_source(it, wrt, L, contract=False):
         lines.append(f"    ExactBins<{W}>::flush(c.pv, const_cast<unsigned char*>(smem), c.gw, c.stats, tid);")
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = sizes[name]
+        if name in it.exact:
+            if ("p", name) in priv:
+                lines.append(f"    ExactSum<{S}>::flush(c.sx{t}, c.x{t}, c.stats, tid, nth);")
+            if ("d", name) in priv:
+                lines.append(f"    ExactSum<{L * S}>::flush(c.sdx{t}, c.dx{t}, c.stats, tid, nth);")
+            continue
         if ("p", name) in priv:
             if dt == T.F32:
                 lines.append(f"    SumPriv<{S}>::flush(c.s{t}, c.g{t}, tid, nth);")
             else:
                 lines.append(f"    for (int b = tid; b < {S}; b += nth) if (c.s{t}[b]) atomicAdd(&c.g{t}[b], c.s{t}[b]);")
     for q, (t, name, shape) in enumerate(ftal):
-        if ("d", name) in priv:
+        if ("d", name) in priv and name not in it.exact:
             lines.append(f"    SumPriv<{L * sizes[name]}>::flush(c.sd{t}, c.gd{t}, tid, nth);")
     lines.append("  }")
+    lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int nth) {")
     if contract:
-        lines.append("  __device__ static void epilogue(const Ctx& c, int tid, int) {")
         lines.append(f"    if (tid == 0) ExactBins<{W}>::readout(c.gw, c.g, c.stats);")
-        lines.append("  }")
-    else:
-        lines.append("  __device__ static void epilogue(const Ctx&, int, int) {}")
+    for t, name in ex:
+        lines.append(f"    ExactSum<{sizes[name]}>::readout(c.x{t}, c.g{t}, c.stats, tid, nth);")
+        if not contract:
+            lines.append(f"    ExactSum<{L * sizes[name]}>::readout(c.dx{t}, c.gd{t}, c.stats, tid, nth);")
+    lines.append("  }")
     lines.append("};")
     lines.append("}  // namespace tmb")
     lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')

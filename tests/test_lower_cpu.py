@@ -275,3 +275,19 @@ def test_per_item_operand_gradient_program():
     assert p0.tallies[0].shape == (1,)
     src = lower.grad_source(L.it, [0], wrt_pi=(0,))[0]
     assert "c.gpi0[item * 1 + 0] =" in src
+
+
+def test_forward_mode_of_fixed_point_outputs():
+    """jvp and the forward-mode value_and_grad of an item with a fixed-point output: its tangent is exact too"""
+    f = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8), fixed_point=True), "hits": tm.Sum((4,), tm.api.torch.int32),
+                                "end": tm.Sum(())},
+                in_axes=(0, 0, 0, None, None), max_steps=64)
+    kx = prng.split(prng.PRNGKey(3), 8)
+    L = f.lowered((np.zeros((8, 3), np.float32), kx, np.full(8, 5, np.int32), np.float32(0.3), np.float32(1.7)))
+    p = L.jvp_program((0, 1), 2)
+    assert [(t.name, t.exact) for t in p.tallies] == [("dep", True), ("hits", False), ("end", False),
+                                                       ("d_dep", True), ("d_end", False)]
+    names = [n for n, _, _, _ in p.result_layout(8)[0]]
+    assert names[:7] == ["dep", "hits", "end", "d_dep", "d_end", "dep.exact", "d_dep.exact"]
+    v = L.vg_program((0, 1))
+    assert [n for n, _, _, _ in v.result_layout(8)[0]][:6] == ["dep", "hits", "end", "ct", "dep.exact", "ct.exact"]

@@ -612,3 +612,33 @@ def test_per_item_operand_gradient(cuda):
     g = gx.cpu().numpy().astype(np.float64)
     assert np.abs(g - want_x).max() <= 1e-4 * np.abs(want_x).max()
     assert abs(float(ga) - want_a) <= 1e-4 * abs(want_a)
+
+
+def test_forward_mode_of_fixed_point_outputs(cuda):
+    """a fixed-point output in forward mode: its tangent tally is exact (bitwise the same under any claim order) and
+    equals the plain tally's tangent within the float tolerance; the forward-mode value_and_grad agrees with the
+    replay (exact_order=True)"""
+    args = _mixer_args(4000, 0.3, 1.7)
+    fx = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8), fixed_point=True), "hits": tm.Sum((4,), torch.int32),
+                                 "end": tm.Sum(())}, in_axes=(0, 0, 0, None, None), max_steps=64)
+    fp = tm.vmap(mixer, outputs={"dep": tm.Sum((8, 8, 8)), "hits": tm.Sum((4,), torch.int32), "end": tm.Sum(())},
+                 in_axes=(0, 0, 0, None, None), max_steps=64)
+    tan = np.array([[1.0, 0.0], [0.0, 1.0]], np.float32)
+    rx, dx = fx.jvp(*args, wrt=(3, 4), tangents=tan)
+    rp, dp = fp.jvp(*args, wrt=(3, 4), tangents=tan)
+    torch.cuda.synchronize()
+    assert near(dx["dep"].cpu().numpy(), dp["dep"].cpu().numpy())
+    assert np.array_equal(bits(rx.outputs["dep"].cpu().numpy()), bits(fx(*args).outputs["dep"].cpu().numpy()))
+    prog = fx.last_lowered.jvp_program((0, 1), 2)
+    outs = []
+    for order in (None, np.arange(4000, dtype=np.int32)[::-1].copy()):
+        o = B.run(prog, list(args[:3]), [args[3], args[4], tan], consts=(64,), order=order)
+        torch.cuda.synchronize()
+        outs.append(o[3].cpu().numpy())
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    cts = {"dep": torch.ones((8, 8, 8)), "end": torch.full((), 0.5)}
+    r1, g1 = fx.value_and_grad(*args, wrt=(3, 4), cotangents=cts)
+    r2, g2 = fx.value_and_grad(*args, wrt=(3, 4), cotangents=cts, exact_order=True)
+    torch.cuda.synchronize()
+    assert near(g1.cpu().numpy(), g2.cpu().numpy())
+    assert np.array_equal(bits(r1.outputs["dep"].cpu().numpy()), bits(r2.outputs["dep"].cpu().numpy()))
