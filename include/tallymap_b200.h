@@ -60,6 +60,11 @@ int tm_register(int64_t id, const void* image, size_t n, const char* note, int32
 int tm_compile_register(int64_t id, const char* source, const char* include_dir, const char* note,
                         int32_t n_buffers, int32_t smem_bytes, int32_t block);
 
+/* Compile as tm_compile_register does, without registering: the cubin's size into *n and, when `out` holds cap >= *n
+ * bytes, the cubin itself (call once with out = NULL for the size).  For a caller that keeps compiled items on disk
+ * and registers them later with tm_register (the reference's disk cubin cache, backends/kernel/__init__.py:71-128). */
+int tm_compile(const char* source, const char* include_dir, int32_t block, void* out, size_t cap, size_t* n);
+
 /* Resources of a kernel on the current device: out[7] = registers per thread, local bytes per thread, static
  * shared bytes per block, resident blocks per SM, SMs, max resident threads per SM, block size.
  * Replaces: tallymap_kernel_info (backends/kernel/shim.cc:147-155). */

@@ -95,6 +95,8 @@ def lib():
         L.tm_probe_threefry.argtypes = [P, i32, P, i64, ctypes.POINTER(i64)]
         L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, i32, P, P, P]
         L.tm_compile_register.argtypes = [i64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]
+        L.tm_compile.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, P, ctypes.c_size_t,
+                                 ctypes.POINTER(ctypes.c_size_t)]
         _HANDLE = L
         return L
 
@@ -108,7 +110,7 @@ def check(rc):
 EXPORTS = ("tm_abi_version", "tm_last_error", "tm_kernel_id", "tm_kernel_name", "tm_register", "tm_kernel_info",
            "tm_launch", "tm_check_status", "tm_exact_combine", "tm_exact_scatter", "tm_exact_scatter_noalloc",
            "tm_probe_threefry", "tm_math_eval", "tm_tree_generations",
-           "tm_compile_register")
+           "tm_compile_register", "tm_compile")
 
 
 def kernel_id(name):

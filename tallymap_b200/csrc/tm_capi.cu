@@ -283,13 +283,11 @@ int load_nvrtc() {
 }
 }  // namespace
 
-int tm_compile_register(int64_t id, const char* source, const char* include_dir, const char* note,
-                        int32_t n_buffers, int32_t smem_bytes, int32_t block) {
-  if (!source || !include_dir) return fail(TM_EINVAL, "tallymap_b200: tm_compile_register: null argument");
+// NVRTC for sm_100a: the cubin of `source` into *cubin (the log in tm_last_error on failure)
+static int compile_cubin(const char* source, const char* include_dir, const char* note, int32_t block,
+                         std::vector<char>* cubin) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    init_registry();
-    if (find(id)) return TM_OK;       // already registered (first registration wins)
     int rc = load_nvrtc();
     if (rc) return rc;
   }
@@ -312,11 +310,35 @@ int tm_compile_register(int64_t id, const char* source, const char* include_dir,
   }
   size_t n = 0;
   g_nvrtc.cubin_size(prog, &n);
-  std::vector<char> cubin(n);
-  if (n) g_nvrtc.cubin(prog, cubin.data());
+  cubin->assign(n, 0);
+  if (n) g_nvrtc.cubin(prog, cubin->data());
   g_nvrtc.destroy(&prog);
   if (n == 0) return fail(TM_EINVAL, "tallymap_b200: NVRTC produced no cubin");
-  return tm_register(id, cubin.data(), n, note, n_buffers, smem_bytes, block);
+  return TM_OK;
+}
+
+int tm_compile_register(int64_t id, const char* source, const char* include_dir, const char* note,
+                        int32_t n_buffers, int32_t smem_bytes, int32_t block) {
+  if (!source || !include_dir) return fail(TM_EINVAL, "tallymap_b200: tm_compile_register: null argument");
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    init_registry();
+    if (find(id)) return TM_OK;       // already registered (first registration wins)
+  }
+  std::vector<char> cubin;
+  const int rc = compile_cubin(source, include_dir, note, block, &cubin);
+  if (rc) return rc;
+  return tm_register(id, cubin.data(), cubin.size(), note, n_buffers, smem_bytes, block);
+}
+
+int tm_compile(const char* source, const char* include_dir, int32_t block, void* out, size_t cap, size_t* n) {
+  if (!source || !include_dir || !n) return fail(TM_EINVAL, "tallymap_b200: tm_compile: null argument");
+  std::vector<char> cubin;
+  const int rc = compile_cubin(source, include_dir, "item", block, &cubin);
+  if (rc) return rc;
+  *n = cubin.size();
+  if (out && cap >= cubin.size()) std::memcpy(out, cubin.data(), cubin.size());
+  return TM_OK;
 }
 
 int tm_kernel_info(int64_t id, long long* out) {

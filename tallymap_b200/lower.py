@@ -547,16 +547,57 @@ def _assign_carry(it, names, state="s"):
 _COMPILED = {}
 
 
+def _headers_digest():
+    """the digest of the runtime headers a lowered source includes: part of a cached cubin's key"""
+    if not hasattr(_headers_digest, "d"):
+        h = hashlib.sha256()
+        for f in sorted(os.listdir(CSRC)):
+            if f.endswith((".cuh", ".h")):
+                with open(os.path.join(CSRC, f), "rb") as fh:
+                    h.update(f.encode() + fh.read())
+        _headers_digest.d = h.hexdigest()
+    return _headers_digest.d
+
+
+def cache_dir():
+    """where compiled items are kept across processes (the reference's disk cubin cache,
+    backends/kernel/__init__.py:71-128): $TALLYMAP_B200_CACHE, else the package's _cache directory, beside its
+    built library; "" disables it"""
+    d = os.environ.get("TALLYMAP_B200_CACHE")
+    return os.path.join(os.path.dirname(CSRC), "_cache") if d is None else d
+
+
 def compile_kernel(source, note, n_buffers, smem_bytes):
     """compile `source` (its entry point `tm_main`) for sm_100a with NVRTC and register it -> kernel id.  Cached per
-    process by the source's digest (the reference's structural kernel cache, backends/kernel/__init__.py:71-128)."""
+    process by the source's digest (the reference's structural kernel cache, backends/kernel/__init__.py:71-128) and
+    on disk by the digest of the source and the runtime headers (a cubin, registered with tm_register)."""
     digest = hashlib.sha256(source.encode()).hexdigest()
     kid = int(digest[:15], 16)          # a positive int64 id
     if kid in _COMPILED:
         return kid
     L = _lib.lib()
-    _lib.check(L.tm_compile_register(ctypes.c_int64(kid), source.encode(), CSRC.encode(), note.encode(),
-                                     n_buffers, smem_bytes, 128))
+    d = cache_dir()
+    path = os.path.join(d, hashlib.sha256((digest + _headers_digest()).encode()).hexdigest() + ".cubin") if d else None
+    image = None
+    if path and os.path.exists(path):
+        with open(path, "rb") as fh:
+            image = fh.read()
+    if image is None:
+        n = ctypes.c_size_t()
+        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, None, 0, ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(n.value)
+        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, buf, n.value, ctypes.byref(n)))
+        image = buf.raw[:n.value]
+        if path:
+            try:
+                os.makedirs(d, exist_ok=True)
+                tmp = f"{path}.{os.getpid()}.tmp"
+                with open(tmp, "wb") as fh:
+                    fh.write(image)
+                os.replace(tmp, path)          # (atomic: a concurrent process sees the whole file or none)
+            except OSError:
+                pass                           # (a read-only home: no disk cache)
+    _lib.check(L.tm_register(ctypes.c_int64(kid), image, len(image), note.encode(), n_buffers, smem_bytes, 128))
     _COMPILED[kid] = note
     from . import backend
     backend.COMPILED[kid] = n_buffers

@@ -291,3 +291,32 @@ def test_forward_mode_of_fixed_point_outputs():
     assert names[:7] == ["dep", "hits", "end", "d_dep", "d_end", "dep.exact", "d_dep.exact"]
     v = L.vg_program((0, 1))
     assert [n for n, _, _, _ in v.result_layout(8)[0]][:6] == ["dep", "hits", "end", "ct", "dep.exact", "ct.exact"]
+
+
+def test_compiled_items_disk_cache(monkeypatch):
+    """a compiled item is kept on disk by the digest of its source and the runtime headers, and a later process
+    (here: a cleared in-process cache) registers the cached cubin instead of compiling again"""
+    import os
+    import shutil
+    d = os.path.join(os.path.dirname(lower.CSRC), "_cache", f"test-{os.getpid()}")
+    monkeypatch.setenv("TALLYMAP_B200_CACHE", d)
+    try:
+        def walk3(t, x, key, drift):          # (a source no other test compiles in this process)
+            def body(c):
+                k, x, t = c
+                u = tl.random.uniform(tl.random.fold_in(key, k))
+                return k + 1, x + 0.03 * (2 * u - 1), t.add("hist", (x * 256).astype(tl.int32), drift * x)
+            k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+            return t, k
+        f = tm.vmap(walk3, outputs={"hist": tm.Sum((256,))}, in_axes=(0, 0, None), max_steps=20000)
+        L = f.lowered(_args_walk())
+        cached = os.listdir(d)
+        assert len(cached) >= 1 and all(p.endswith(".cubin") for p in cached)
+        kid = L.fwd.kernel
+        lower._COMPILED.pop(kid)
+        calls = []
+        monkeypatch.setattr(lower._lib.lib(), "tm_compile", lambda *a: calls.append(a) or 1)
+        assert lower.compile_kernel(L.fwd_source, "walk_fwd", 12, 16) == kid
+        assert not calls
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
