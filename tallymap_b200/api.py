@@ -101,6 +101,8 @@ class Family:
     fused: dict = dataclasses.field(default_factory=dict)   # the same keys -> value-and-grad program (one launch)
     onepass: dict = dataclasses.field(default_factory=dict)  # the same keys -> one-pass value-and-grad (no active
                                                               # carry: step VJPs summed as the forward runs)
+    onepass_grad: bool = False   # grad(exact_order=False) runs the one-pass launch: it is forward mode, while the
+                                 # replay re-runs the forward
 
 
 FAMILIES = {
@@ -108,10 +110,11 @@ FAMILIES = {
                          {(0,): B.Q1_VG1}),
     "walk1d": Family("walk1d", B.RW_FWD, {(0,): B.RW_GRAD}, (0, 0, None), 20000, {(0,): B.RW_VG},
                      {(0,): B.RW_VG1}),
-    "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000, {}, {(0, 1): B.PH_VG1}),
+    "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000, {}, {(0, 1): B.PH_VG1},
+                     onepass_grad=True),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
-    "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000),
+    "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000, onepass_grad=True),
 }
 
 
@@ -217,7 +220,7 @@ class Mapped:
         photon, the shower), that launch instead, its forward outputs discarded -- faster than the replay, which
         re-runs the forward, and equal to it within the float tolerance."""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
-        if not exact_order and self.fam.name in ("photon", "shower"):
+        if not exact_order and self.fam.onepass_grad:
             return self.value_and_grad(*args, wrt=wrt, cotangents=cotangents)[1]
         if "tree" in self.fam.grads:
             return self._tree_grad(args, idx, cotangents, wrt)
