@@ -158,6 +158,13 @@ def _eval(e, a):
             return F32(np.sqrt(F32(a[0])))
     if p == "floor":
         return F32(np.floor(a[0]))
+    if p == "round":
+        return F32(np.rint(F32(a[0])))
+    if p == "rem":
+        with np.errstate(all="ignore"):
+            return F32(np.fmod(F32(a[0]), F32(a[1])))
+    if p == "stop":
+        return a[0]
     if p == "abs":
         return F32(abs(a[0])) if d == T.F32 else _wrap32(abs(a[0]))
     if p == "max":

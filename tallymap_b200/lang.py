@@ -1,8 +1,8 @@
 """The operations an item function may use, for tracing (tallymap_b200.trace): a scalar subset of jax.numpy,
 jax.random and lax.while_loop with jax's semantics, the ones the reference's op table lowers for these items
 (tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
-random_bits / fold_in / split, while), and compositions of them with jax's semantics (clip, sign, square,
-random.bernoulli).
+random_bits / fold_in / split, while, round, rem, stop_gradient), and compositions of them with jax's semantics
+(clip, sign, square, mod, the reductions sum / max / min / all / any over a per-item vector, random.bernoulli).
 
     from tallymap_b200 import lang as tl
 
@@ -95,6 +95,75 @@ def where(c, a, b):
     if a.dtype != b.dtype:
         raise T.TraceError(f"tallymap_b200.lang.where of {a.dtype} and {b.dtype}")
     return T._cur().emit("select", [c, a, b], [a.dtype])[0]
+
+
+def round(x):   # noqa: A001 (jnp.round)
+    """jnp.round: to the nearest integer, ties to even"""
+    return _f32("round", x)
+
+
+def stop_gradient(x):
+    """lax.stop_gradient: the value itself, with no derivative (no cotangent, no tangent) through it"""
+    x = T._lit(x)
+    if isinstance(x, T.Lit):
+        return x
+    return T._cur().emit("stop", [x], [x.dtype])[0]
+
+
+def rem(a, b):
+    """lax.rem of float32: C's fmod (the sign of a)"""
+    r = T._binary("rem", a, b)
+    if r.dtype != T.F32:
+        raise T.TraceError("tallymap_b200.lang.rem takes float32 (use % for integers)")
+    return r
+
+
+def mod(a, b):
+    """jnp.mod / jnp.remainder of float32: the sign of b (rem, plus b when the signs differ)"""
+    r = rem(a, b)
+    return where((r != 0.0) & ((r < 0.0) != (b < 0.0)), r + b, r)
+
+
+def sum(xs):   # noqa: A001 (jnp.sum of a per-item vector)
+    """jnp.sum of a tuple of scalars (a per-item vector), added left to right"""
+    xs = tuple(xs)
+    out = xs[0]
+    for x in xs[1:]:
+        out = out + x
+    return out
+
+
+def max(xs):   # noqa: A001 (jnp.max of a per-item vector)
+    """jnp.max of a tuple of scalars: lax.max left to right"""
+    xs = tuple(xs)
+    out = xs[0]
+    for x in xs[1:]:
+        out = maximum(out, x)
+    return out
+
+
+def min(xs):   # noqa: A001 (jnp.min of a per-item vector)
+    xs = tuple(xs)
+    out = xs[0]
+    for x in xs[1:]:
+        out = minimum(out, x)
+    return out
+
+
+def all(bs):   # noqa: A001 (jnp.all of a tuple of bools)
+    bs = tuple(bs)
+    out = bs[0]
+    for b in bs[1:]:
+        out = out & b
+    return out
+
+
+def any(bs):   # noqa: A001 (jnp.any of a tuple of bools)
+    bs = tuple(bs)
+    out = bs[0]
+    for b in bs[1:]:
+        out = out | b
+    return out
 
 
 def clip(x, a_min, a_max):

@@ -87,6 +87,12 @@ def c_expr(e, a):
         return f"__fsqrt_rn({a[0]})"
     if p == "floor":
         return f"floorf({a[0]})"
+    if p == "round":    # jnp.round: to nearest, ties to even (an exact operation: host and device agree)
+        return f"rintf({a[0]})"
+    if p == "rem":      # lax.rem of f32: C's fmodf, exact
+        return f"fmodf({a[0]}, {a[1]})"
+    if p == "stop":     # lax.stop_gradient: the value itself
+        return f"({a[0]})"
     if p == "abs":
         return f"fabsf({a[0]})" if d == T.F32 else f"tm_iabs({a[0]})"
     if p == "pow":
@@ -613,7 +619,7 @@ def _active(it, wrt, extra=()):
 
     def prop(eqns):
         for e in eqns:
-            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor") or not e.outs:
+            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop") or not e.outs:
                 continue
             if any(isinstance(x, T.Var) and x.id in act for x in e.ins):
                 for o in e.outs:
@@ -712,8 +718,13 @@ class _Rev:
         elif p == "convert":
             if x[0].dtype == T.F32 and e.outs[0].dtype == T.F32:
                 self.add(x[0], g)
-        elif p == "floor":
+        elif p in ("floor", "round", "stop"):
             pass
+        elif p == "rem":
+            # lax.rem's transpose (jax: d/dx = 1, d/dy = -sign(x / y) * floor(|x / y|))
+            q = f"({a[0]} / {a[1]})"
+            self.add(x[0], g)
+            self.add(x[1], f"((-{g}) * (({q} > 0.0f ? 1.0f : ({q} < 0.0f ? -1.0f : {q})) * floorf(fabsf({q}))))")
         else:
             raise LowerError(f"tallymap_b200.lower: no reverse rule for {p}")
 
@@ -1224,8 +1235,12 @@ def _jvp_rule(e, a, d, out):
         return f"({a[0]} ? {db or '0.0f'} : {dc or '0.0f'})"
     if p == "convert":
         return x if e.outs[0].dtype == T.F32 and e.ins[0].dtype == T.F32 else None
-    if p == "floor":
+    if p in ("floor", "round", "stop"):
         return None
+    if p == "rem":
+        q = f"({a[0]} / {a[1]})"
+        return plus(x, None if y is None else
+                    f"((-{y}) * (({q} > 0.0f ? 1.0f : ({q} < 0.0f ? -1.0f : {q})) * floorf(fabsf({q}))))")
     raise LowerError(f"tallymap_b200.lower: no jvp rule for {p}")
 
 

@@ -167,3 +167,24 @@ def affine(t, x, key, a):
         return k + 1, x, t
     k, x, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
     return t, x
+
+
+def rounding(t, a, key, n, s):
+    """round, rem, mod and the vector reductions on awkward values, recorded so that they compare bitwise"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        v = (x * s, u - 0.5, x * u)
+        t = t.append("rec", {"r": tl.round(x * 2.5), "m": tl.rem(x, s + u), "o": tl.mod(x, u - 0.6),
+                             "s": tl.sum(v), "x": tl.max(v), "n": tl.min(v),
+                             "a": (tl.all((x > 0.0, u > 0.5)) | tl.any((x < -5.0, u < 0.1))).astype(tl.int32)})
+        return k + 1, x * (1.5 - u) - 0.75, t
+    k, x, t = tl.while_loop(lambda c: c[0] < n, body, (0, a, t))
+    return t, k
+
+
+def stopped(t, x, key, a):
+    """rem and stop_gradient in the emitted value: d/da = x (rem's derivative in its first argument is 1, the
+    stopped term contributes nothing)"""
+    t = t.add("h", 0, tl.rem(x * a, 0.7) + tl.stop_gradient(a) * x)
+    return t, x

@@ -642,3 +642,45 @@ def test_forward_mode_of_fixed_point_outputs(cuda):
     torch.cuda.synchronize()
     assert near(g1.cpu().numpy(), g2.cpu().numpy())
     assert np.array_equal(bits(r1.outputs["dep"].cpu().numpy()), bits(r2.outputs["dep"].cpu().numpy()))
+
+
+def test_lowered_round_rem_reductions_against_ir_evaluator(cuda):
+    """round, rem, mod, sum / max / min / all / any on awkward values, bitwise through Records"""
+    from items_lang import rounding
+    vals = np.float32([np.nan, np.inf, -np.inf, -0.0, 0.0, 1e38, -1e38, 3e-39, -7.5, 7.5, 0.6, 123456.0, -2.0, 2.5])
+    n = len(vals)
+    keys = prng.split(prng.PRNGKey(29), n)
+    args = (vals, keys, np.full(n, 4, np.int32), np.float32(0.7))
+    fields = {"r": torch.float32, "m": torch.float32, "o": torch.float32, "s": torch.float32, "x": torch.float32,
+              "n": torch.float32, "a": torch.int32}
+    f = tm.vmap(rounding, outputs={"rec": tm.Records(fields, capacity=128)}, in_axes=(0, 0, 0, None), max_steps=10)
+    r = f(*args)
+    torch.cuda.synchronize()
+    recspec = {"rec": (128, tuple((k, "f32" if v == torch.float32 else "i32") for k, v in sorted(fields.items())))}
+    ref = _eval(rounding, ["f32", "key", "i32", "f32"], 3, {}, recspec, args, 10)
+    m = len(ref["records"]["rec"])
+    assert m == 4 * n
+    got = {k: v.cpu().numpy() for k, v in r.outputs["rec"].items()}
+    for j, (fname, _) in enumerate(recspec["rec"][1]):
+        want = np.array([rec[j] for rec in ref["records"]["rec"]])
+        g = got[fname][:m]
+        if g.dtype == np.float32:
+            w = want.astype(np.float32)
+            same = (g.view(np.uint32) == w.view(np.uint32)) | (np.isnan(g) & np.isnan(w))
+            assert same.all(), fname
+        else:
+            assert np.array_equal(g.astype(np.int64), want.astype(np.int64)), fname
+
+
+def test_stop_gradient_and_rem_derivatives(cuda):
+    """d/da of sum(rem(x a, 0.7) + stop_gradient(a) x) = sum(x): the replay, the one-pass program and forward mode"""
+    from items_lang import stopped
+    x, k = rw_inputs(100000, seed=41)
+    f = tm.vmap(stopped, outputs={"h": tm.Sum(())}, in_axes=(0, 0, None))
+    want = float(x.astype(np.float64).sum())
+    g1 = f.grad(x, k, np.float32(1.3), wrt=2, cotangents={"h": torch.ones(())})
+    g2 = f.value_and_grad(x, k, np.float32(1.3), wrt=2, cotangents={"h": torch.ones(())})[1]
+    _, d = f.jvp(x, k, np.float32(1.3), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    for g in (float(g1), float(g2), float(d["h"])):
+        assert abs(g - want) <= 1e-5 * abs(want)
