@@ -2,7 +2,8 @@
 jax.random and lax.while_loop with jax's semantics, the ones the reference's op table lowers for these items
 (tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
 random_bits / fold_in / split, while, round, rem, stop_gradient), and compositions of them with jax's semantics
-(clip, sign, square, mod, the reductions sum / max / min / all / any over a per-item vector, random.bernoulli).
+(clip, sign, square, mod, log1p, expm1, tanh, the reductions sum / max / min / all / any over a per-item vector,
+random.bernoulli).
 
     from tallymap_b200 import lang as tl
 
@@ -164,6 +165,30 @@ def any(bs):   # noqa: A001 (jnp.any of a tuple of bools)
     for b in bs[1:]:
         out = out | b
     return out
+
+
+def log1p(x):
+    """jnp.log1p, by Goldberg's method (What Every Computer Scientist Should Know About Floating-Point Arithmetic,
+    1991, Theorem 4): u = 1 + x; x itself where u rounds to 1, else log(u) * (x / (u - 1)), whose rounding error in
+    u cancels; +inf for +inf"""
+    u = 1.0 + x
+    return where((u == 1.0) | (u == float("inf")), x, log(u) * (x / (u - 1.0)))
+
+
+def expm1(x):
+    """jnp.expm1, by Kahan's method: u = exp(x); x where u rounds to 1, -1 where u - 1 does, u itself where it
+    overflows, else (u - 1) * (x / log(u))"""
+    u = exp(x)
+    um = u - 1.0
+    return where(u == 1.0, x, where(um == -1.0, -1.0, where(u == float("inf"), u, um * (x / log(u)))))
+
+
+def tanh(x):
+    """jnp.tanh from expm1: with e = expm1(-2|x|), tanh(|x|) = -e / (e + 2), the sign of x restored (tanh(-0) = -0)"""
+    ax = abs(x)
+    e = expm1(-2.0 * ax)
+    t = (-e) / (e + 2.0)
+    return where(x < 0.0, -t, where(x > 0.0, t, x))
 
 
 def clip(x, a_min, a_max):

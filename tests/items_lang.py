@@ -188,3 +188,9 @@ def stopped(t, x, key, a):
     stopped term contributes nothing)"""
     t = t.add("h", 0, tl.rem(x * a, 0.7) + tl.stop_gradient(a) * x)
     return t, x
+
+
+def transcend(t, x, key, s):
+    """log1p, expm1 and tanh (compositions: Goldberg's and Kahan's methods), recorded"""
+    t = t.append("rec", {"l": tl.log1p(x), "e": tl.expm1(x * s), "h": tl.tanh(x)})
+    return t, x

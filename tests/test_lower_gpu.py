@@ -684,3 +684,33 @@ def test_stop_gradient_and_rem_derivatives(cuda):
     torch.cuda.synchronize()
     for g in (float(g1), float(g2), float(d["h"])):
         assert abs(g - want) <= 1e-5 * abs(want)
+
+
+def test_log1p_expm1_tanh(cuda):
+    """the compositions bitwise against the IR evaluator, and within 8 ulp of float64 references where finite"""
+    from items_lang import transcend
+    rng = np.random.default_rng(3)
+    vals = np.concatenate([np.float32([np.nan, np.inf, -np.inf, -0.0, 0.0, -1.0, -0.999999, 1e-30, -1e-30, 3e-39, 88.0,
+                                       -88.0, 20.0, -20.0]),
+                           rng.uniform(-0.99, 10.0, 2000).astype(np.float32),
+                           (10.0 ** rng.uniform(-20, 0, 2000)).astype(np.float32)])
+    n = len(vals)
+    keys = prng.split(prng.PRNGKey(2), n)
+    fields = {"l": torch.float32, "e": torch.float32, "h": torch.float32}
+    f = tm.vmap(transcend, outputs={"rec": tm.Records(fields, capacity=n)}, in_axes=(0, 0, None))
+    r = f(vals, keys, np.float32(1.0))
+    torch.cuda.synchronize()
+    recspec = {"rec": (n, tuple((k, "f32") for k in sorted(fields)))}
+    ref = _eval(transcend, ["f32", "key", "f32"], 2, {}, recspec, (vals, keys, np.float32(1.0)), 1)
+    got = {k: v.cpu().numpy() for k, v in r.outputs["rec"].items()}
+    x64 = vals.astype(np.float64)
+    with np.errstate(all="ignore"):
+        exact = {"l": np.log1p(x64), "e": np.expm1(x64), "h": np.tanh(x64)}
+    for j, fname in enumerate(sorted(fields)):
+        want = np.array([rec[j] for rec in ref["records"]["rec"]], np.float32)
+        g = got[fname][:n]
+        assert ((g.view(np.uint32) == want.view(np.uint32)) | (np.isnan(g) & np.isnan(want))).all(), fname
+        e = exact[fname]
+        ok = np.isfinite(e) & (np.abs(e) < 3e38)
+        ulp = np.abs(g[ok].astype(np.float64) - e[ok]) / np.spacing(np.abs(e[ok]).astype(np.float32)).astype(np.float64)
+        assert ulp.max() <= 8, (fname, ulp.max())
