@@ -2,8 +2,8 @@
 jax.random and lax.while_loop with jax's semantics, the ones the reference's op table lowers for these items
 (tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
 random_bits / fold_in / split, while, round, rem, stop_gradient), and compositions of them with jax's semantics
-(clip, sign, square, mod, log1p, expm1, tanh, the reductions sum / max / min / all / any over a per-item vector,
-random.bernoulli).
+(clip, sign, square, mod, log1p, expm1, tanh, the reductions sum / max / min / all / any, cumsum and searchsorted
+over a per-item vector, random.bernoulli).
 
     from tallymap_b200 import lang as tl
 
@@ -189,6 +189,29 @@ def tanh(x):
     e = expm1(-2.0 * ax)
     t = (-e) / (e + 2.0)
     return where(x < 0.0, -t, where(x > 0.0, t, x))
+
+
+def cumsum(xs):
+    """jnp.cumsum of a per-item vector (a tuple): the running sums, added left to right"""
+    out = []
+    acc = None
+    for x in xs:
+        acc = x if acc is None else acc + x
+        out.append(acc)
+    return tuple(out)
+
+
+def searchsorted(a, v, side="left"):
+    """jnp.searchsorted of v in the sorted per-item vector a: the count of elements < v (side "left") or <= v
+    ("right"), as int32"""
+    if side not in ("left", "right"):
+        raise T.TraceError("tallymap_b200.lang.searchsorted: side 'left' or 'right'")
+    cnt = None
+    for x in a:
+        c = (x < v) if side == "left" else (x <= v)
+        c = c.astype(int32)
+        cnt = c if cnt is None else cnt + c
+    return cnt
 
 
 def clip(x, a_min, a_max):

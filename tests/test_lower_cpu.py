@@ -320,3 +320,20 @@ def test_compiled_items_disk_cache(monkeypatch):
         assert not calls
     finally:
         shutil.rmtree(d, ignore_errors=True)
+
+
+def test_vector_compositions_trace():
+    """cumsum and searchsorted over a per-item vector trace to the expected scalar equations"""
+    def item(t, p, key, a):
+        c = tl.cumsum(p)
+        i = tl.searchsorted(c, a)
+        t = t.add("h", i, 1)
+        return t, c[2]
+    tr = T.trace_item(item, [("f32", 3), "key", "f32"], 2, {"h": ((4,), "i32")})
+    prims = [e.prim for e in tr.post]
+    assert prims.count("add") >= 2 + 2 and prims.count("lt") == 3 and prims.count("emit") == 1
+    from oracle.ir_eval import Evaluator
+    p = np.float32([[0.1, 0.2, 0.3], [0.5, 0.5, 0.5]])
+    r = Evaluator(tr, 10).run([p, prng.split(prng.PRNGKey(0), 2)], [0.45])
+    assert list(r["sums"]["h"]) == [1, 0, 1, 0]        # cumsums (0.1, 0.3, 0.6) and (0.5, 1, 1.5) against 0.45
+    assert np.allclose(r["results"][0], [0.6, 1.5])
