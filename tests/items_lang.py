@@ -194,3 +194,23 @@ def transcend(t, x, key, s):
     """log1p, expm1 and tanh (compositions: Goldberg's and Kahan's methods), recorded"""
     t = t.append("rec", {"l": tl.log1p(x), "e": tl.expm1(x * s), "h": tl.tanh(x)})
     return t, x
+
+
+def birth_death(t, x0, key, c0, c1):
+    """an exact stochastic simulation (Gillespie's direct method) of a birth-death process: X -> X + 1 at rate
+    c[0] * 50, X -> X - 1 at rate c[1] * X; run to time 2, the final count tallied into a histogram, the mean time
+    step and the event count per item"""
+    def body(s):
+        k, tt, x, t = s
+        xf = x.astype(tl.float32)
+        a = (tl.maximum(c0 * 50.0, 0.0), tl.maximum(c1 * xf, 0.0))
+        a0 = tl.sum(a)
+        u = tl.random.uniform(tl.random.fold_in(key, k), (2,))
+        tau = -tl.log(tl.maximum(u[0], 1e-20)) / tl.maximum(a0, 1e-20)
+        r = tl.clip(tl.searchsorted(tl.cumsum(a), u[1] * a0, side="right"), 0, 1)
+        x = tl.clip(x + tl.where(r == 0, 1, -1), 0, 1000)
+        t = t.add("tau", 0, tau)
+        return k + 1, tt + tau, x, t
+    k, tt, x, t = tl.while_loop(lambda s: s[1] < 2.0, body, (0, 0.0, x0, t))
+    t = t.add("hist", tl.clip(x // 8, 0, 31), 1)
+    return t, x, k

@@ -714,3 +714,26 @@ def test_log1p_expm1_tanh(cuda):
         ok = np.isfinite(e) & (np.abs(e) < 3e38)
         ulp = np.abs(g[ok].astype(np.float64) - e[ok]) / np.spacing(np.abs(e[ok]).astype(np.float32)).astype(np.float64)
         assert ulp.max() <= 8, (fname, ulp.max())
+
+
+def test_gillespie_birth_death(cuda):
+    """an exact SSA item (a float-time loop, a propensity vector, cumsum / searchsorted selection, int clips):
+    per-item final counts and event counts and the integer histogram bitwise against the IR evaluator"""
+    from items_lang import birth_death
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    n = 500
+    x0 = np.random.default_rng(4).integers(0, 200, n).astype(np.int32)
+    keys = prng.split(prng.PRNGKey(17), n)
+    c = (np.float32(1.0), np.float32(0.4))
+    f = tm.vmap(birth_death, outputs={"hist": tm.Sum((32,), torch.int32), "tau": tm.Sum(())},
+                in_axes=(0, 0, None, None), max_steps=1 << 16)
+    r = f(x0, keys, *c)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    tr = T.trace_item(birth_death, ["i32", "key", "f32", "f32"], 2, {"hist": ((32,), "i32"), "tau": ((), "f32")})
+    ref = Evaluator(tr, 1 << 16).run([x0, keys], list(c))
+    xs, ks = r.per_item
+    assert np.array_equal(xs.cpu().numpy(), ref["results"][0]) and np.array_equal(ks.cpu().numpy(), ref["results"][1])
+    assert np.array_equal(r.outputs["hist"].cpu().numpy(), ref["sums"]["hist"])
+    assert near(np_out(r)["tau"], ref["sums"]["tau"])
