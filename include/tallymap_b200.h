@@ -62,8 +62,12 @@ int tm_compile_register(int64_t id, const char* source, const char* include_dir,
 
 /* Compile as tm_compile_register does, without registering: the cubin's size into *n and, when `out` holds cap >= *n
  * bytes, the cubin itself (call once with out = NULL for the size).  For a caller that keeps compiled items on disk
- * and registers them later with tm_register (the reference's disk cubin cache, backends/kernel/__init__.py:71-128). */
-int tm_compile(const char* source, const char* include_dir, int32_t block, void* out, size_t cap, size_t* n);
+ * and registers them later with tm_register (the reference's disk cubin cache, backends/kernel/__init__.py:71-128).
+ *   flags: bit 0 (TM_COMPILE_FMAD): FMA contraction of float multiply-adds (--fmad=true), the reference's
+ *          cuda_math='fast' (backends/kernel/__init__.py:141-146); 0: --fmad=false, as tm_compile_register */
+#define TM_COMPILE_FMAD 1
+int tm_compile(const char* source, const char* include_dir, int32_t block, int32_t flags, void* out, size_t cap,
+               size_t* n);
 
 /* Resources of a kernel on the current device: out[7] = registers per thread, local bytes per thread, static
  * shared bytes per block, resident blocks per SM, SMs, max resident threads per SM, block size.

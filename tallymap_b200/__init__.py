@@ -11,9 +11,9 @@ Layers (top down):
 """
 from . import lang, prng
 from ._lib import TallymapError, build
-from .api import FAMILIES, Queue, Records, Result, Sum, vmap
+from .api import FAMILIES, Queue, Records, Result, Sum, TallyError, UnsupportedError, vmap
 from .backend import PROGRAMS, STATS, ItemProgram, TSpec, run
 
 __version__ = "0.1.0"
-__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "Queue", "Records", "Result", "Sum", "TSpec", "TallymapError", "build", "lang",
-           "prng", "run", "vmap"]
+__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "Queue", "Records", "Result", "Sum", "TSpec", "TallyError",
+           "TallymapError", "UnsupportedError", "build", "lang", "prng", "run", "vmap"]

@@ -95,7 +95,7 @@ def lib():
         L.tm_probe_threefry.argtypes = [P, i32, P, i64, ctypes.POINTER(i64)]
         L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, i32, P, P, P]
         L.tm_compile_register.argtypes = [i64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]
-        L.tm_compile.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, P, ctypes.c_size_t,
+        L.tm_compile.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, i32, P, ctypes.c_size_t,
                                  ctypes.POINTER(ctypes.c_size_t)]
         _HANDLE = L
         return L

@@ -25,6 +25,8 @@ import numpy as np
 import torch
 
 from . import backend as B
+from . import trace as T
+from .trace import TallyError, UnsupportedError  # noqa: F401  (the reference's public exception types)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -136,8 +138,9 @@ def _poison(outs, bad):
 class Mapped:
     """tallymap.vmap(item, outputs, in_axes, max_steps) over a lowered item family."""
 
-    def __init__(self, fam, outputs, in_axes, max_steps, spawn=None):
+    def __init__(self, fam, outputs, in_axes, max_steps, spawn=None, opts=None):
         self.fam = fam
+        self.opts = opts or options()
         if spawn is not None and not fam.fwd.spawns:
             raise ValueError(f"tallymap_b200: item {fam.name!r} does not spawn")
         self.queue = spawn.capacity if spawn is not None else None
@@ -240,7 +243,8 @@ class Mapped:
             c = cotangents.get(t.name)
             n = int(pi[0].shape[0]) if pi else 0
             cts.append(torch.zeros(t.dims(n), dtype=t.dtype) if c is None else c)
-        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order,
+                    rev_checkpoints=self.opts["rev_checkpoints"])
         ct = out[0].reshape(-1)[sel]
         trunc = out[len(prog.tallies) + 1 + prog.trunc]
         ct = torch.where(trunc.bool().any(), torch.full_like(ct, float("nan")), ct)
@@ -270,7 +274,8 @@ class Mapped:
             return None
         pi, bc = self._split(args)
         n = int(pi[0].shape[0]) if pi else 0
-        out = B.run(prog, pi, list(bc) + self._cotangents(n, cotangents), consts=(self.max_steps,))
+        out = B.run(prog, pi, list(bc) + self._cotangents(n, cotangents), consts=(self.max_steps,),
+                    rev_checkpoints=self.opts["rev_checkpoints"])
         p = self.fam.fwd
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
@@ -315,7 +320,8 @@ class Mapped:
         pi, bc = self._split(args)
         c = cotangents.get("dep")
         ct = torch.zeros(512, dtype=torch.float32) if c is None else c
-        r = self.fam.grads["tree"](pi, bc[0], ct, max_steps=self.max_steps)
+        r = self.fam.grads["tree"](pi, bc[0], ct, max_steps=self.max_steps,
+                                   rev_checkpoints=self.opts["rev_checkpoints"])
         by_arg = {0: r["ct_E"], 1: r["ct_depth"], 3: r["ct_X0"].reshape(())}
         if any(w not in by_arg for w in idx):
             raise ValueError(f"tallymap_b200: item {self.fam.name!r} is differentiable in arguments {sorted(by_arg)}")
@@ -334,8 +340,9 @@ class MappedFn:
     operand signature, lowered to CUDA and compiled for sm_100a at run time (tallymap_b200.lower, NVRTC); the reverse
     programs are lowered and compiled on the first gradient request for each set of differentiated operands."""
 
-    def __init__(self, fn, outputs, in_axes, max_steps, spawn=None):
+    def __init__(self, fn, outputs, in_axes, max_steps, spawn=None, opts=None):
         self.fn = fn
+        self.opts = opts or options()
         if spawn is not None and not isinstance(spawn, Queue):
             raise TypeError("tallymap_b200: spawn= takes a tallymap_b200.Queue(capacity)")
         self.spawn = spawn
@@ -349,6 +356,12 @@ class MappedFn:
                 raise TypeError(f"tallymap_b200: output {name!r}: Sum of float32 or int32")
             self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32",
                                   bool(getattr(o, "fixed_point", False)))
+        if in_axes == 0:
+            import inspect
+            ps = list(inspect.signature(fn).parameters.values())[1:]
+            if any(q.kind in (q.VAR_POSITIONAL, q.VAR_KEYWORD) for q in ps):
+                raise TypeError("tallymap_b200: an item with *args takes in_axes as a tuple (0 or None per argument)")
+            in_axes = (0,) * len(ps)
         self.in_axes = tuple(in_axes)
         if any(ax not in (0, None) for ax in self.in_axes):
             raise ValueError("tallymap_b200: in_axes entries are 0 (per item) or None (broadcast)")
@@ -391,7 +404,12 @@ class MappedFn:
                     args_[pos] = x
                 return self.fn(t, *args_)
             item.__name__ = getattr(self.fn, "__name__", "item")
-            self._lowered[key] = lower.Lowered(item, pis + bcs, len(pis), self.outputs, spawn=self.spawn is not None)
+            L = lower.Lowered(item, pis + bcs, len(pis), self.outputs, spawn=self.spawn is not None,
+                              math=self.opts["math"], min_blocks=self.opts["min_blocks"])
+            if self.opts["schedule"] == "step" and isinstance(L.tr.cond_out, T.Lit):
+                raise UnsupportedError(f"tallymap_b200: schedule='step' needs an item with exactly one top-level "
+                                       f"while loop; {item.__name__} has none")
+            self._lowered[key] = L
         self.last_lowered = self._lowered[key]
         return self._lowered[key]
 
@@ -450,7 +468,8 @@ class MappedFn:
                 continue
             c = cotangents.get(name)
             cts.append(torch.zeros(shape, dtype=torch.float32) if c is None else c)
-        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order)
+        out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order,
+                    rev_checkpoints=self.opts["rev_checkpoints"])
         ct = out[0].reshape(-1)
         ys = out[2:]
         bad = ys[prog.trunc].bool().any()
@@ -552,11 +571,67 @@ class MappedFn:
         return res, (ct.reshape(()) if isinstance(wrt, int) else ct)
 
 
-def vmap(item, outputs, in_axes, max_steps=None, spawn=None):
-    """tallymap.vmap: `item` is a Python function written against tallymap_b200.lang (traced, lowered and compiled
-    on first call) or the name of a built-in lowered family ("quickstart", "walk1d", "photon", "lorenz",
-    "shower").  spawn: a Queue, for an item that spawns children with t.spawn (_api.py:88-98, 426-433)."""
-    if callable(item) and not isinstance(item, Family):
-        return MappedFn(item, outputs, in_axes, max_steps, spawn)
-    fam = FAMILIES[item] if isinstance(item, str) else item
-    return Mapped(fam, outputs, in_axes, max_steps, spawn)
+OPTIONS = ("cuda_math", "schedule", "min_blocks_per_sm", "xla_batch_size", "rev_checkpoints", "rev_stats")
+BACKENDS = ("auto", "xla")
+
+
+def options(backend="auto", **opts):
+    """the call options of tallymap.vmap (_api.py:414-425, 493-507), validated -> dict(math, schedule, min_blocks,
+    rev_checkpoints).
+      cuda_math          'ieee' (this backend's default: correctly rounded f32 division and square root, bitwise
+                         against the CPU evaluator and across GPU counts) | 'approx' (the reference's default:
+                         div.full / sqrt.approx) | 'fast' (approx plus FMA contraction of float multiply-adds;
+                         statistical only).  Lowered items only: the built-in families are compiled ahead of time
+                         with 'ieee'
+      schedule           'item' | 'step': both run this runtime's step-granular refill (a warp runs the item loop
+                         while every lane steps and refills a lane whose item ended); 'step' also demands an item
+                         with exactly one top-level while loop, as the reference's does
+      min_blocks_per_sm  None | N in 1..32: the lowered entry point's __launch_bounds__(block, N)
+      rev_checkpoints    'auto' (default) | C >= 1: the replay adjoint's states per checkpoint buffer
+      rev_stats          accepted; the tree adjoint's counters are always kept (Mapped.last_tree)
+      xla_batch_size     accepted for the reference's xla backend, which this build does not have
+    backend: 'auto' (the kernel backend) | 'xla' (the reference's plain-JAX interpreter: UnsupportedError here)"""
+    from . import lower
+    bad = sorted(set(opts) - set(OPTIONS))
+    if bad:
+        raise ValueError(f"tallymap_b200: unknown option(s) {bad}; options are {', '.join(OPTIONS)}")
+    if backend not in BACKENDS:
+        raise ValueError(f"tallymap_b200: unknown backend {backend!r}; backends are {', '.join(BACKENDS)}")
+    if backend == "xla":
+        raise UnsupportedError("tallymap_b200: backend='xla' is the reference's plain-JAX interpreter, which needs "
+                               "JAX; this package is the kernel backend (backend='auto')")
+    math = opts.get("cuda_math") or "ieee"
+    if math not in lower.MATH_MODES:
+        raise ValueError(f"tallymap_b200: cuda_math must be 'ieee', 'approx' or 'fast', got {math!r}")
+    schedule = opts.get("schedule", "item")
+    if schedule not in ("item", "step"):
+        raise ValueError(f"tallymap_b200: schedule must be 'item' or 'step', got {schedule!r}")
+    mb = opts.get("min_blocks_per_sm")
+    if mb is not None and (isinstance(mb, bool) or not isinstance(mb, (int, np.integer)) or not 1 <= int(mb) <= 32):
+        raise ValueError(f"tallymap_b200: min_blocks_per_sm must be None or an integer in 1..32, got {mb!r}")
+    rc = opts.get("rev_checkpoints", "auto")
+    if rc == "auto" or rc is None:
+        rc = None
+    elif isinstance(rc, bool) or not isinstance(rc, (int, np.integer)) or int(rc) < 1:
+        raise ValueError(f"tallymap_b200: rev_checkpoints must be 'auto' or an integer >= 1, got {rc!r}")
+    return dict(math=math, schedule=schedule, min_blocks=None if mb is None else int(mb),
+                rev_checkpoints=None if rc is None else int(rc))
+
+
+def vmap(fn=None, *, outputs, in_axes=0, max_steps=None, spawn=None, backend="auto", **opts):
+    """tallymap.vmap (_api.py:428-507): `fn` is a Python function written against tallymap_b200.lang (traced,
+    lowered and compiled on first call) or the name of a built-in lowered family ("quickstart", "walk1d", "photon",
+    "lorenz", "shower"); with fn=None, a decorator.  in_axes: 0 (every argument per item), or 0 / None per argument.
+    spawn: a Queue, for an item that spawns children with t.spawn (_api.py:88-98, 426-433).  opts: see options()."""
+    if fn is None:
+        return lambda f: vmap(f, outputs=outputs, in_axes=in_axes, max_steps=max_steps, spawn=spawn,
+                              backend=backend, **opts)
+    o = options(backend, **opts)
+    if callable(fn) and not isinstance(fn, Family):
+        return MappedFn(fn, outputs, in_axes, max_steps, spawn, o)
+    fam = FAMILIES[fn] if isinstance(fn, str) else fn
+    if o["math"] != "ieee" or o["min_blocks"] is not None:
+        raise UnsupportedError(f"tallymap_b200: the built-in item {fam.name!r} is compiled ahead of time with "
+                               "cuda_math='ieee' and its own launch bounds (cuda_math / min_blocks_per_sm apply to "
+                               "lowered items)")
+    return Mapped(fam, outputs, fam.in_axes if in_axes == 0 else in_axes, max_steps, spawn, o)

@@ -284,7 +284,7 @@ int load_nvrtc() {
 }  // namespace
 
 // NVRTC for sm_100a: the cubin of `source` into *cubin (the log in tm_last_error on failure)
-static int compile_cubin(const char* source, const char* include_dir, const char* note, int32_t block,
+static int compile_cubin(const char* source, const char* include_dir, const char* note, int32_t block, int32_t flags,
                          std::vector<char>* cubin) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -297,8 +297,8 @@ static int compile_cubin(const char* source, const char* include_dir, const char
   const std::string inc = std::string("-I") + include_dir;
   char blk[32];
   std::snprintf(blk, sizeof(blk), "-DTM_BLOCK=%d", block);
-  const char* opts[] = {"-arch=sm_100a", "-std=c++17", "--fmad=false", "-lineinfo", inc.c_str(),
-                        "-I/usr/local/cuda/include", blk};
+  const char* fmad = (flags & 1) ? "--fmad=true" : "--fmad=false";
+  const char* opts[] = {"-arch=sm_100a", "-std=c++17", fmad, "-lineinfo", inc.c_str(), "-I/usr/local/cuda/include", blk};
   const int crc = g_nvrtc.compile(prog, 7, opts);
   if (crc != 0) {
     size_t n = 0;
@@ -326,15 +326,17 @@ int tm_compile_register(int64_t id, const char* source, const char* include_dir,
     if (find(id)) return TM_OK;       // already registered (first registration wins)
   }
   std::vector<char> cubin;
-  const int rc = compile_cubin(source, include_dir, note, block, &cubin);
+  const int rc = compile_cubin(source, include_dir, note, block, 0, &cubin);
   if (rc) return rc;
   return tm_register(id, cubin.data(), cubin.size(), note, n_buffers, smem_bytes, block);
 }
 
-int tm_compile(const char* source, const char* include_dir, int32_t block, void* out, size_t cap, size_t* n) {
+int tm_compile(const char* source, const char* include_dir, int32_t block, int32_t flags, void* out, size_t cap,
+               size_t* n) {
   if (!source || !include_dir || !n) return fail(TM_EINVAL, "tallymap_b200: tm_compile: null argument");
+  if (flags & ~1) return fail(TM_EINVAL, "tallymap_b200: tm_compile: unknown flags %d", (int)flags);
   std::vector<char> cubin;
-  const int rc = compile_cubin(source, include_dir, "item", block, &cubin);
+  const int rc = compile_cubin(source, include_dir, "item", block, flags, &cubin);
   if (rc) return rc;
   *n = cubin.size();
   if (out && cap >= cubin.size()) std::memcpy(out, cubin.data(), cubin.size());

@@ -31,8 +31,8 @@ SPAWN_STACK_SHARED = 8   # a lane's private stack entries in shared memory (csrc
 TDTYPE = {T.F32: torch.float32, T.I32: torch.int32, T.U32: torch.int32, T.BOOL: torch.uint8}
 
 
-class LowerError(TypeError):
-    pass
+class LowerError(T.UnsupportedError):
+    """a traced item (or a derived program of it) this lowering does not produce"""
 
 
 # ------------------------------------------------------------------------------------------------ C expressions
@@ -62,6 +62,8 @@ def c_expr(e, a):
     p, d = e.prim, e.ins[0].dtype if e.ins else None
     if p in ("add", "sub", "mul") and d in (T.I32,):
         return f"(i32)((u32)({a[0]}) {_BIN[p]} (u32)({a[1]}))"         # wrapping int32 arithmetic
+    if p == "div":      # f32 only ('/' of integers does not trace); the call's cuda_math decides the instruction
+        return f"tm_fdiv({a[0]}, {a[1]})"
     if p in _BIN:
         return f"({a[0]} {_BIN[p]} {a[1]})"
     if p == "idiv":
@@ -84,7 +86,7 @@ def c_expr(e, a):
     if p in _MATH:
         return f"{_MATH[p]}({a[0]})"
     if p == "sqrt":
-        return f"__fsqrt_rn({a[0]})"
+        return f"tm_fsqrt({a[0]})"
     if p == "floor":
         return f"floorf({a[0]})"
     if p == "round":    # jnp.round: to nearest, ties to even (an exact operation: host and device agree)
@@ -150,7 +152,30 @@ __device__ __forceinline__ i32 tm_floormod(i32 a, i32 b) {
 }
 __device__ __forceinline__ u32 tm_floordiv(u32 a, u32 b) { return b ? a / b : 0u; }
 __device__ __forceinline__ u32 tm_floormod(u32 a, u32 b) { return b ? a % b : 0u; }
+// f32 division and square root by the call's cuda_math: 'ieee' (no define) correctly rounded; 'approx' and 'fast'
+// the f32 PTX XLA:GPU emits, div.full (at most 2 ulp) and sqrt.approx (backends/kernel/__init__.py:9-12, 141-146)
+#if defined(TM_MATH_APPROX) || defined(TM_MATH_FAST)
+__device__ __forceinline__ float tm_fdiv(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float tm_fsqrt(float a) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+#else
+__device__ __forceinline__ float tm_fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float tm_fsqrt(float a) { return __fsqrt_rn(a); }
+#endif
 }  // namespace tmb
+// the entry point's launch bounds: min_blocks_per_sm=N caps registers for N resident blocks per SM
+#ifdef TM_MIN_BLOCKS
+#define TM_MAIN_BOUNDS __launch_bounds__(TM_BLOCK, TM_MIN_BLOCKS)
+#else
+#define TM_MAIN_BOUNDS __launch_bounds__(TM_BLOCK)
+#endif
 """
 
 
@@ -514,7 +539,7 @@ def forward_source(it, standalone=True):
     if not standalone:
         return "\n".join(lines[2:]), max(smem, 16)
     lines.append("}  // namespace tmb")
-    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append('extern "C" __global__ void TM_MAIN_BOUNDS tm_main(const tmb::Params P, const long long n) {')
     lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenFwd>(P, n);")
     lines.append("}")
     return "\n".join(lines), max(smem, 16)
@@ -573,11 +598,31 @@ def cache_dir():
     return os.path.join(os.path.dirname(CSRC), "_cache") if d is None else d
 
 
-def compile_kernel(source, note, n_buffers, smem_bytes):
+MATH_MODES = ("ieee", "approx", "fast")
+
+
+def options_source(math="ieee", min_blocks=None):
+    """-> (the defines a call's options put before a lowered source, tm_compile flags).  math: the reference's
+    cuda_math (backends/kernel/__init__.py:141-146) -- 'ieee' correctly rounded f32 division and square root (this
+    backend's default: bitwise against the CPU evaluator); 'approx' div.full / sqrt.approx; 'fast' approx plus FMA
+    contraction of float multiply-adds.  min_blocks: the entry point's __launch_bounds__(block, min_blocks).  The
+    defaults add nothing, so a default source is unchanged."""
+    if math not in MATH_MODES:
+        raise ValueError(f"tallymap_b200: cuda_math must be one of {MATH_MODES}, got {math!r}")
+    head = "" if math == "ieee" else f"#define TM_MATH_{math.upper()} 1\n"
+    if min_blocks is not None:
+        if int(min_blocks) < 1 or int(min_blocks) > 32:
+            raise ValueError(f"tallymap_b200: min_blocks_per_sm must be in 1..32, got {min_blocks!r}")
+        head += f"#define TM_MIN_BLOCKS {int(min_blocks)}\n"
+    return head, (1 if math == "fast" else 0)
+
+
+def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
     """compile `source` (its entry point `tm_main`) for sm_100a with NVRTC and register it -> kernel id.  Cached per
     process by the source's digest (the reference's structural kernel cache, backends/kernel/__init__.py:71-128) and
-    on disk by the digest of the source and the runtime headers (a cubin, registered with tm_register)."""
-    digest = hashlib.sha256(source.encode()).hexdigest()
+    on disk by the digest of the source and the runtime headers (a cubin, registered with tm_register).  flags:
+    tm_compile's (1: FMA contraction); a nonzero value enters the digest."""
+    digest = hashlib.sha256(source.encode() + (b"" if not flags else f"/flags={flags}".encode())).hexdigest()
     kid = int(digest[:15], 16)          # a positive int64 id
     if kid in _COMPILED:
         return kid
@@ -590,9 +635,9 @@ def compile_kernel(source, note, n_buffers, smem_bytes):
             image = fh.read()
     if image is None:
         n = ctypes.c_size_t()
-        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, None, 0, ctypes.byref(n)))
+        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, flags, None, 0, ctypes.byref(n)))
         buf = ctypes.create_string_buffer(n.value)
-        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, buf, n.value, ctypes.byref(n)))
+        _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, flags, buf, n.value, ctypes.byref(n)))
         image = buf.raw[:n.value]
         if path:
             try:
@@ -689,12 +734,12 @@ class _Rev:
             self.add(x[0], f"({g} * {a[1]})")
             self.add(x[1], f"({a[0]} * {g})")
         elif p == "div":
-            self.add(x[0], f"({g} / {a[1]})")
-            self.add(x[1], f"(((-{g}) * {a[0]}) * (1.0f / ({a[1]} * {a[1]})))")
+            self.add(x[0], f"tm_fdiv({g}, {a[1]})")
+            self.add(x[1], f"(((-{g}) * {a[0]}) * tm_fdiv(1.0f, ({a[1]} * {a[1]})))")
         elif p == "neg":
             self.add(x[0], f"(-{g})")
         elif p == "log":
-            self.add(x[0], f"({g} / {a[0]})")
+            self.add(x[0], f"tm_fdiv({g}, {a[0]})")
         elif p == "exp":
             self.add(x[0], f"({g} * {out})")
         elif p == "sin":
@@ -702,7 +747,7 @@ class _Rev:
         elif p == "cos":
             self.add(x[0], f"((-{g}) * tmm::sinf({a[0]}))")
         elif p == "sqrt":
-            self.add(x[0], f"({g} * (0.5f / {out}))")
+            self.add(x[0], f"({g} * tm_fdiv(0.5f, {out}))")
         elif p == "pow":
             self.add(x[0], f"({g} * ({a[1]} * tmm::powf({a[0]}, {a[1]} - 1.0f)))")
             self.add(x[1], f"({g} * (tmm::logf({a[0]}) * {out}))")
@@ -722,7 +767,7 @@ class _Rev:
             pass
         elif p == "rem":
             # lax.rem's transpose (jax: d/dx = 1, d/dy = -sign(x / y) * floor(|x / y|))
-            q = f"({a[0]} / {a[1]})"
+            q = f"tm_fdiv({a[0]}, {a[1]})"
             self.add(x[0], g)
             self.add(x[1], f"((-{g}) * (({q} > 0.0f ? 1.0f : ({q} < 0.0f ? -1.0f : {q})) * floorf(fabsf({q}))))")
         else:
@@ -970,7 +1015,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     if not standalone:
         return "\n".join(lines[2:]), stored_bytes, smem_bytes
     lines.append("}  // namespace tmb")
-    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append('extern "C" __global__ void TM_MAIN_BOUNDS tm_main(const tmb::Params P, const long long n) {')
     lines.append("  tmb::replay_body<tmb::GenGrad, 1>(P, n);")
     lines.append("}")
     lines.append(f"static_assert(tmb::GenGrad::kSmemBytes == {smem_bytes}, \"shared-memory size\");")
@@ -1021,7 +1066,7 @@ def onepass_source(it, wrt):
              "typedef OnePassVG<GenFwd, GenGrad, GenVGMap> GenVG;",
              "static_assert(GenFwd::kNBuf == GenVGMap::kNF && GenGrad::kNBuf == GenVGMap::kNG, \"buffer maps\");",
              "}  // namespace tmb",
-             'extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {',
+             'extern "C" __global__ void TM_MAIN_BOUNDS tm_main(const tmb::Params P, const long long n) {',
              "  tmb::forward_body<tmb::GenVG>(P, n);",
              "}",
              f"static_assert(tmb::GenVG::kSmemBytes == {smem}, \"shared-memory size\");"]
@@ -1042,9 +1087,11 @@ class Lowered:
     """a traced item's programs: the forward (compiled at construction) and its reverse programs (compiled per set
     of differentiated broadcast operands, on first use)"""
 
-    def __init__(self, fn, in_specs, n_per_item, outputs, name=None, spawn=False):
+    def __init__(self, fn, in_specs, n_per_item, outputs, name=None, spawn=False, math="ieee", min_blocks=None):
         from .backend import ItemProgram, TSpec
         self.name = name or getattr(fn, "__name__", "item")
+        self.head, self.flags = options_source(math, min_blocks)
+        self.math, self.min_blocks = math, min_blocks
         recs = {k: (v[1], tuple(v[2])) for k, v in outputs.items() if v[0] == "records"}
         outputs = {k: v for k, v in outputs.items() if v[0] != "records"}
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
@@ -1069,7 +1116,7 @@ class Lowered:
             # the spawn runtime's shared stack entries after the item's block (csrc/tm_spawn.cuh SpawnSmem)
             smem = (smem + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * len(it.loads) * 128
             src += f"\nstatic_assert(tmb::SpawnSmem<tmb::GenFwd>::kBytes == {smem}, \"shared-memory size\");"
-        kid = compile_kernel(src, self.name + "_fwd", nbuf, smem)
+        kid = self._compile(src, self.name + "_fwd", nbuf, smem)
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc,
                                consts=("max_steps", "queue") if sp else ("max_steps",), tallies=tallies,
                                ys=ys, trunc=len(ys) - 1, records=records, spawns=sp,
@@ -1078,6 +1125,10 @@ class Lowered:
         self.grads = {}
         self.jvps = {}
         self.vgs = {}
+
+    def _compile(self, src, note, nbuf, smem):
+        """compile one of this item's programs with the call's options (cuda_math, min_blocks_per_sm)"""
+        return compile_kernel(self.head + src, note, nbuf, smem, self.flags)
 
     def jvp_program(self, wrt, lanes):
         """the forward-mode program: the forward's outputs and, per tangent lane, the tangents of its float tallies
@@ -1099,7 +1150,7 @@ class Lowered:
             sp = self.it.spawns
             nx = sum(1 for t in tallies if t.exact)
             nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + 2 + len(self.fwd.ys) + (3 if sp else 0)
-            kid = compile_kernel(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
+            kid = self._compile(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
             self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc,
                                          consts=("max_steps", "queue") if sp else ("max_steps",),
                                          tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc, spawns=sp,
@@ -1130,13 +1181,13 @@ class Lowered:
                 tallies = self.fwd.tallies + (TSpec("ct", (len(wrt),), exact=True),)
                 if not sp and not has_active_carry(self.it, list(wrt)):
                     src, smem, nbuf = onepass_source(self.it, list(wrt))
-                    kid = compile_kernel(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
+                    kid = self._compile(src, f"{self.name}_vg{''.join(map(str, wrt))}", nbuf, smem)
                 elif len(wrt) <= FWD_GRAD_MAX:
                     # forward mode; through spawn, each child carries its float leaves' tangents
                     src, smem = jvp_source(self.it, list(wrt), len(wrt), contract=True)
                     nx = sum(1 for t in tallies if t.exact)
                     nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + 2 + len(self.fwd.ys) + (3 if sp else 0)
-                    kid = compile_kernel(src, f"{self.name}_fg{''.join(map(str, wrt))}", nbuf, smem)
+                    kid = self._compile(src, f"{self.name}_fg{''.join(map(str, wrt))}", nbuf, smem)
                 else:
                     kid = None
                 if kid is not None:
@@ -1171,7 +1222,7 @@ class Lowered:
             ys += (_operand("truncated", T.BOOL),)
             nbuf = len(self.pi) + len(bc) + 2 + 4 + len(ys) + 1
             tag = "".join(map(str, wrt)) + ("_pi" + "".join(map(str, wrt_pi)) if wrt_pi else "")
-            kid = compile_kernel(src, f"{self.name}_grad{tag}", nbuf, smem)
+            kid = self._compile(src, f"{self.name}_grad{tag}", nbuf, smem)
             self.grads[key] = ItemProgram(f"{self.name}_grad", kid, pi=self.pi, bc=bc,
                                           consts=("max_steps", "rev_checkpoints", "replay_threads"),
                                           tallies=(TSpec("ct", (max(len(wrt), 1),), exact=True),),
@@ -1206,12 +1257,12 @@ def _jvp_rule(e, a, d, out):
     if p == "mul":
         return plus(None if x is None else f"({x} * {a[1]})", None if y is None else f"({a[0]} * {y})")
     if p == "div":
-        return plus(None if x is None else f"({x} / {a[1]})",
-                    None if y is None else f"(((-{y}) * {a[0]}) * (1.0f / ({a[1]} * {a[1]})))")
+        return plus(None if x is None else f"tm_fdiv({x}, {a[1]})",
+                    None if y is None else f"(((-{y}) * {a[0]}) * tm_fdiv(1.0f, ({a[1]} * {a[1]})))")
     if p == "neg":
         return None if x is None else f"(-{x})"
     if p == "log":
-        return None if x is None else f"({x} / {a[0]})"
+        return None if x is None else f"tm_fdiv({x}, {a[0]})"
     if p == "exp":
         return None if x is None else f"({x} * {out})"
     if p == "sin":
@@ -1219,7 +1270,7 @@ def _jvp_rule(e, a, d, out):
     if p == "cos":
         return None if x is None else f"((-{x}) * tmm::sinf({a[0]}))"
     if p == "sqrt":
-        return None if x is None else f"({x} * (0.5f / {out}))"
+        return None if x is None else f"({x} * tm_fdiv(0.5f, {out}))"
     if p == "pow":
         return plus(None if x is None else f"({x} * ({a[1]} * tmm::powf({a[0]}, {a[1]} - 1.0f)))",
                     None if y is None else f"({y} * (tmm::logf({a[0]}) * {out}))")
@@ -1238,7 +1289,7 @@ def _jvp_rule(e, a, d, out):
     if p in ("floor", "round", "stop"):
         return None
     if p == "rem":
-        q = f"({a[0]} / {a[1]})"
+        q = f"tm_fdiv({a[0]}, {a[1]})"
         return plus(x, None if y is None else
                     f"((-{y}) * (({q} > 0.0f ? 1.0f : ({q} < 0.0f ? -1.0f : {q})) * floorf(fabsf({q}))))")
     raise LowerError(f"tallymap_b200.lower: no jvp rule for {p}")
@@ -1641,7 +1692,7 @@ def jvp_source(it, wrt, L, contract=False):
     lines.append("  }")
     lines.append("};")
     lines.append("}  // namespace tmb")
-    lines.append('extern "C" __global__ void __launch_bounds__(TM_BLOCK) tm_main(const tmb::Params P, const long long n) {')
+    lines.append('extern "C" __global__ void TM_MAIN_BOUNDS tm_main(const tmb::Params P, const long long n) {')
     lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenJvp>(P, n);")
     lines.append("}")
     lines.append(f"static_assert(tmb::GenJvp::kSmemBytes == {max(smem, 16)}, \"shared-memory size\");")

@@ -22,7 +22,17 @@ _CTX = []
 
 
 class TraceError(TypeError):
-    pass
+    """an item function this tracer cannot trace (a type error in the item, or a construct outside the language)"""
+
+
+class UnsupportedError(TraceError, NotImplementedError):
+    """a valid item whose construct the kernel backend does not lower (tallymap/_api.py:198 UnsupportedError, a
+    NotImplementedError there too); never a fallback: nothing else runs the item"""
+
+
+class TallyError(TraceError):
+    """the tally handle used in a way a write-through tally cannot honour: read as a value, dropped from the carry,
+    or moved to another carry position (tallymap/_rewrite.py:31 TallyError)"""
 
 
 @dataclasses.dataclass(frozen=True)
@@ -77,6 +87,8 @@ def _lit(x, like=None):
         if like is not None and like.dtype in (I32, U32):
             raise TraceError("tallymap_b200.lang: a float literal combined with an integer value (use astype)")
         return Lit(float(x), F32)
+    if isinstance(x, TallyToken):
+        raise TallyError("tallymap_b200.lang: the tally handle is not a value (it is written with t.add, not read)")
     raise TraceError(f"tallymap_b200.lang: unsupported operand {x!r}")
 
 
@@ -361,9 +373,10 @@ def while_loop(cond_fun, body_fun, init):
     tr = _cur()
     st = getattr(tr, "loop_state", None)
     if st is None or st.get("depth", 0) != 0:
-        raise TraceError("tallymap_b200.lang: only ONE top-level while_loop per item (nested loops are not lowered)")
+        raise UnsupportedError("tallymap_b200.lang: only ONE top-level while_loop per item "
+                               "(nested loops are not lowered)")
     if st.get("done"):
-        raise TraceError("tallymap_b200.lang: only one top-level while_loop per item")
+        raise UnsupportedError("tallymap_b200.lang: only one top-level while_loop per item")
     flat_in, rebuild = _flatten(init)
     carry = []
     body_tr = Trace(tr.ids)
@@ -395,7 +408,7 @@ def while_loop(cond_fun, body_fun, init):
         raise TraceError("tallymap_b200.lang: the loop body must return a carry of the same structure")
     for a, b in zip(flat_in, flat_out):
         if isinstance(a, TallyToken) != isinstance(b, TallyToken):
-            raise TraceError("tallymap_b200.lang: the tally handle must stay in its carry position")
+            raise TallyError("tallymap_b200.lang: the tally handle must stay in its carry position")
     # the loop's results: fresh variables (the final carry)
     post = [x if isinstance(x, TallyToken) else tr.new(x.dtype) for x in carry]
     st.update(done=True, init=[x for x in flat_in], carry=cvars, cond=cond_tr.eqns, cond_out=c,
@@ -462,17 +475,19 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
                   post_carry=[], pre_len=0)
     out = out if isinstance(out, tuple) else (out,)
     if not out or not isinstance(out[0], TallyToken):
-        raise TraceError("tallymap_b200.lang: an item returns (t, *per_item_results)")
+        raise TallyError("tallymap_b200.lang: an item returns (t, *per_item_results)")
     results = [_lit(r) for r in out[1:]]
     pre = tr.eqns[:st["pre_len"]]
     post = tr.eqns[st["pre_len"]:]
     keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
     if any(e.prim == "append" for e in pre):
-        raise TraceError("tallymap_b200.lang: append before the loop is not lowered (append in the loop or after it)")
+        raise UnsupportedError("tallymap_b200.lang: append before the loop is not lowered "
+                               "(append in the loop or after it)")
     if any(e.prim == "spawn" for e in pre):
-        raise TraceError("tallymap_b200.lang: spawn before the loop is not lowered (spawn in the loop or after it)")
+        raise UnsupportedError("tallymap_b200.lang: spawn before the loop is not lowered "
+                               "(spawn in the loop or after it)")
     if sum(e.prim == "spawn" for e in st["body"]) > 2 or sum(e.prim == "spawn" for e in post) > 2:
-        raise TraceError("tallymap_b200.lang: at most two spawns per loop step and two after the loop")
+        raise UnsupportedError("tallymap_b200.lang: at most two spawns per loop step and two after the loop")
     return Traced(inputs=args, n_per_item=n_per_item, pre=pre, carry_in=[_lit(x) for x in keep(st["init"])],
                   carry=keep(st["carry"]), cond=st["cond"], cond_out=st["cond_out"], body=st["body"],
                   body_out=[_lit(x) for x in keep(st["body_out"])], post_carry=keep(st["post_carry"]), post=post,

@@ -214,3 +214,14 @@ def birth_death(t, x0, key, c0, c1):
     k, tt, x, t = tl.while_loop(lambda s: s[1] < 2.0, body, (0, 0.0, x0, t))
     t = t.add("hist", tl.clip(x // 8, 0, 31), 1)
     return t, x, k
+
+
+def divided(t, x, key, a):
+    """a walk whose control flow has no division or square root; the values it tallies divide and take roots"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("h", tl.clip((x * 16).astype(tl.int32), 0, 15), tl.sqrt(u) / (a + x))
+        return k + 1, x + 0.05 * (2 * u - 1), t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    return t, k

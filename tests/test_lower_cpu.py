@@ -337,3 +337,94 @@ def test_vector_compositions_trace():
     r = Evaluator(tr, 10).run([p, prng.split(prng.PRNGKey(0), 2)], [0.45])
     assert list(r["sums"]["h"]) == [1, 0, 1, 0]        # cumsums (0.1, 0.3, 0.6) and (0.5, 1, 1.5) against 0.45
     assert np.allclose(r["results"][0], [0.6, 1.5])
+
+
+def test_vmap_options_validated():
+    """tallymap.vmap's options (_api.py:414-425, 493-507): unknown names, bad values and backend='xla' raise"""
+    outs = {"hist": tm.Sum((256,)), "side": tm.Sum((2,))}
+    for bad in ({"cuda_math": "exact"}, {"schedule": "warp"}, {"min_blocks_per_sm": 0}, {"min_blocks_per_sm": 33},
+                {"min_blocks_per_sm": True}, {"rev_checkpoints": 0}, {"rev_checkpoints": "some"}, {"fill": 1}):
+        with pytest.raises(ValueError):
+            tm.vmap(walk, outputs=outs, in_axes=(0, 0, None), **bad)
+    with pytest.raises(ValueError):
+        tm.vmap(walk, outputs=outs, in_axes=(0, 0, None), backend="cuda")
+    with pytest.raises(tm.UnsupportedError) as e:
+        tm.vmap(walk, outputs=outs, in_axes=(0, 0, None), backend="xla")
+    assert isinstance(e.value, NotImplementedError)
+    with pytest.raises(tm.UnsupportedError):      # the built-in families are compiled ahead of time with 'ieee'
+        tm.vmap("walk1d", outputs=outs, in_axes=(0, 0, None), cuda_math="approx")
+    f = tm.vmap(walk, outputs=outs, in_axes=(0, 0, None), cuda_math="approx", schedule="step", min_blocks_per_sm=4,
+                rev_checkpoints=8, rev_stats=True, xla_batch_size=1024)
+    assert f.opts == dict(math="approx", schedule="step", min_blocks=4, rev_checkpoints=8)
+
+
+def test_vmap_decorator_and_default_in_axes():
+    """@tm.vmap(outputs=..., ...) as a decorator; in_axes=0 maps every argument after the tally"""
+    @tm.vmap(outputs={"h": tm.Sum((8,))}, max_steps=10)
+    def item(t, x, key):
+        return t.add("h", (x * 8).astype(tl.int32), 1.0)
+    assert isinstance(item, tm.api.MappedFn) and item.in_axes == (0, 0)
+    g = tm.vmap("walk1d", outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, max_steps=100)
+    assert g.fam.in_axes == (0, 0, None)
+
+
+def test_cuda_math_and_min_blocks_sources():
+    """cuda_math='approx' / 'fast' put div.full / sqrt.approx behind tm_fdiv / tm_fsqrt (and 'fast' compiles with FMA
+    contraction); min_blocks_per_sm sets the entry point's launch bounds; the default source is unchanged"""
+    def item(t, x, key, a):
+        def body(c):
+            k, x, t = c
+            u = tl.random.uniform(tl.random.fold_in(key, k))
+            return k + 1, x + a * tl.sqrt(u) / (1.0 + x), t.add("h", (x * 8).astype(tl.int32), x / a)
+        k, x, t = tl.while_loop(lambda c: c[1] < 1.0, body, (0, x, t))
+        return t, k
+    outs = {"h": tm.Sum((8,))}
+    args = _args_walk()
+    ids = {}
+    for math, mb in (("ieee", None), ("approx", None), ("fast", None), ("ieee", 4)):
+        f = tm.vmap(item, outputs=outs, in_axes=(0, 0, None), max_steps=100, cuda_math=math, min_blocks_per_sm=mb)
+        L = f.lowered(args)
+        body = L.fwd_source.split("struct GenFwd")[1]
+        assert "tm_fdiv(" in body and "tm_fsqrt(" in body and " / " not in body
+        assert L.head == lower.options_source(math, mb)[0] and L.flags == (math == "fast")
+        g = L.grad_program((0,))
+        ids[(math, mb)] = (L.fwd.kernel, g.kernel)
+    assert len({v for v in ids.values()}) == 4
+    assert lower.options_source("ieee") == ("", 0)
+    assert lower.options_source("approx", 2)[0] == "#define TM_MATH_APPROX 1\n#define TM_MIN_BLOCKS 2\n"
+
+
+def test_schedule_step_needs_a_loop():
+    """schedule='step' raises UnsupportedError for an item with no top-level while loop (_api.py:447-452)"""
+    def flat(t, x):
+        return t.add("h", 0, x)
+    f = tm.vmap(flat, outputs={"h": tm.Sum((1,))}, in_axes=(0,), schedule="step")
+    with pytest.raises(tm.UnsupportedError):
+        f.lowered((np.float32([1.0, 2.0]),))
+    g = tm.vmap(flat, outputs={"h": tm.Sum((1,))}, in_axes=(0,), schedule="item")
+    assert g.lowered((np.float32([1.0, 2.0]),)).fwd.kernel > 0
+
+
+def test_error_types():
+    """the reference's exception types: a Tally read as a value is a TallyError (_rewrite.py:31), a construct the
+    kernel backend does not lower an UnsupportedError (a NotImplementedError, _api.py:198); both TraceErrors here"""
+    def reads(t, x):
+        return t, x + t
+    def nested(t, x):
+        def body(c):
+            i, t = c
+            j, t = tl.while_loop(lambda d: d[0] < 2, lambda d: (d[0] + 1, d[1]), (0, t))
+            return i + j, t
+        i, t = tl.while_loop(lambda c: c[0] < 4, body, (0, t))
+        return t, i
+    def drops(t, x):
+        return x
+    specs = {"h": ((1,), "f32")}
+    with pytest.raises(tm.TallyError):
+        T.trace_item(reads, ["f32"], 1, specs)
+    with pytest.raises(tm.TallyError):
+        T.trace_item(drops, ["f32"], 1, specs)
+    with pytest.raises(tm.UnsupportedError) as e:
+        T.trace_item(nested, ["f32"], 1, specs)
+    assert isinstance(e.value, NotImplementedError) and isinstance(e.value, T.TraceError)
+    assert issubclass(lower.LowerError, tm.UnsupportedError)

@@ -737,3 +737,32 @@ def test_gillespie_birth_death(cuda):
     assert np.array_equal(xs.cpu().numpy(), ref["results"][0]) and np.array_equal(ks.cpu().numpy(), ref["results"][1])
     assert np.array_equal(r.outputs["hist"].cpu().numpy(), ref["sums"]["hist"])
     assert near(np_out(r)["tau"], ref["sums"]["tau"])
+
+
+def test_call_options(cuda):
+    """the call options (_api.py:414-425): cuda_math='approx' (div.full / sqrt.approx) changes the tallied values
+    within a few ulp and no control flow; 'fast' (also FMA contraction) agrees statistically; min_blocks_per_sm
+    changes no bit of a fixed-point output; rev_checkpoints changes the replay's buffers, not the gradient"""
+    from items_lang import divided
+    n = 300
+    x, k = rw_inputs(n, seed=23)
+    a = np.float32(0.7)
+    ref = _eval(divided, ["f32", "key", "f32"], 2, {"h": ((16,), "f32")}, {}, (x, k, a), 20000, exact=("h",))
+    run = lambda **o: tm.vmap(divided, outputs={"h": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None),
+                              max_steps=20000, **o)
+    r0 = run()(x, k, a)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(r0.outputs["h"].cpu().numpy()), bits(ref["sums"]["h"]))
+    assert np.array_equal(r0.per_item.cpu().numpy(), ref["results"][0])
+    r1 = run(cuda_math="approx")(x, k, a)
+    assert np.array_equal(r1.per_item.cpu().numpy(), ref["results"][0])
+    assert near(r1.outputs["h"].cpu().numpy(), ref["sums"]["h"], 2e-6)
+    r2 = run(cuda_math="fast")(x, k, a)
+    same = (r2.per_item.cpu().numpy() == ref["results"][0]).mean()
+    assert same > 0.95 and near(r2.outputs["h"].cpu().numpy(), ref["sums"]["h"], 0.05)
+    r3 = run(min_blocks_per_sm=8)(x, k, a)
+    assert np.array_equal(bits(r3.outputs["h"].cpu().numpy()), bits(r0.outputs["h"].cpu().numpy()))
+    ct = {"h": torch.linspace(-1, 1, 16)}
+    g0 = run().grad(x, k, a, wrt=2, cotangents=ct)
+    g1 = run(rev_checkpoints=4).grad(x, k, a, wrt=2, cotangents=ct)
+    assert near(g1.cpu().numpy(), g0.cpu().numpy())
