@@ -384,7 +384,10 @@ class MappedFn:
             return "key"                      # uint32[N, 2] key data (int32 bits on torch)
         if per_item and len(shape) == 1 and dt == "f32":
             return ("f32", shape[0])
-        raise TypeError(f"tallymap_b200: operand of per-item shape {shape} and dtype {dt} is not lowered")
+        if not per_item and len(shape) == 1 and dt in ("f32", "i32") and 1 <= shape[0] <= BC_VECTOR_MAX:
+            return (dt, shape[0])             # a broadcast vector: that many broadcast scalars
+        raise TypeError(f"tallymap_b200: operand of {'per-item ' if per_item else ''}shape {shape} and dtype {dt} "
+                        "is not lowered")
 
     def lowered(self, args):
         from . import lower
@@ -397,15 +400,27 @@ class MappedFn:
             order = [ax for ax in self.in_axes]
             # the item's arguments in their declared order; the lowering wants per-item first
             perm = [i for i, ax in enumerate(order) if ax == 0] + [i for i, ax in enumerate(order) if ax is None]
+            bargs = [i for i, ax in enumerate(order) if ax is None]
+            # a broadcast vector is lowered as consecutive broadcast scalars: argument -> (first, n or None)
+            groups, leaves = {}, []
+            for i, sp in zip(bargs, bcs):
+                groups[i] = (len(leaves), sp[1] if isinstance(sp, tuple) else None)
+                leaves += [sp[0]] * sp[1] if isinstance(sp, tuple) else [sp]
+            npi = len(pis)
 
             def item(t, *xs):
-                args_ = [None] * len(xs)
-                for pos, x in zip(perm, xs):
+                vals = list(xs[:npi])
+                for i in bargs:
+                    f, n = groups[i]
+                    vals.append(xs[npi + f] if n is None else tuple(xs[npi + f:npi + f + n]))
+                args_ = [None] * len(vals)
+                for pos, x in zip(perm, vals):
                     args_[pos] = x
                 return self.fn(t, *args_)
             item.__name__ = getattr(self.fn, "__name__", "item")
-            L = lower.Lowered(item, pis + bcs, len(pis), self.outputs, spawn=self.spawn is not None,
+            L = lower.Lowered(item, pis + leaves, npi, self.outputs, spawn=self.spawn is not None,
                               math=self.opts["math"], min_blocks=self.opts["min_blocks"])
+            L.bc_groups = groups
             if self.opts["schedule"] == "step" and isinstance(L.tr.cond_out, T.Lit):
                 raise UnsupportedError(f"tallymap_b200: schedule='step' needs an item with exactly one top-level "
                                        f"while loop; {item.__name__} has none")
@@ -414,9 +429,33 @@ class MappedFn:
         return self._lowered[key]
 
     def _split(self, args):
+        """(per-item operands, broadcast scalars): a broadcast vector gives one scalar per element"""
         pi = [a for a, ax in zip(args, self.in_axes) if ax == 0]
-        bc = [a for a, ax in zip(args, self.in_axes) if ax is None]
+        bc = []
+        for a, ax in zip(args, self.in_axes):
+            if ax is None:
+                t = a if isinstance(a, torch.Tensor) else B._host(a)
+                bc += [t[i] for i in range(t.shape[0])] if t.ndim == 1 else [a]
         return pi, bc
+
+    def _bleaves(self, L, idx):
+        """-> (the broadcast scalar positions of broadcast arguments idx, in order; argument -> (its first position
+        among them, n for a vector or None for a scalar))"""
+        pos, where = [], {}
+        for w in idx:
+            f, n = L.bc_groups[w]
+            where[w] = (len(pos), n)
+            pos += [f] if n is None else list(range(f, f + n))
+        return tuple(pos), where
+
+    @staticmethod
+    def _per_arg(ct, where, wrt, idx):
+        """a broadcast gradient vector (one entry per scalar position) -> one gradient per argument: a scalar for
+        a scalar argument, f32[n] for a vector; the flat vector itself for a tuple of scalar arguments"""
+        if all(n is None for _, n in where.values()) and not isinstance(wrt, int):
+            return ct
+        got = {w: ct[q].reshape(()) if n is None else ct[q:q + n] for w, (q, n) in where.items()}
+        return got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx)
 
     def __call__(self, *args):
         L = self.lowered(args)
@@ -457,7 +496,7 @@ class MappedFn:
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
         bidx = [w for w in idx if self.in_axes[w] is None]
         pidx = [w for w in idx if self.in_axes[w] == 0]
-        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in bidx)
+        bpos, where = self._bleaves(L, bidx)
         ppos = tuple(sum(1 for ax in self.in_axes[:w] if ax == 0) for w in pidx)
         prog = L.grad_program(bpos, ppos)
         pi, bc = self._split(args)
@@ -475,15 +514,15 @@ class MappedFn:
         bad = ys[prog.trunc].bool().any()
         nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
         if not pidx:
-            ct = nan(ct)
-            return ct.reshape(()) if isinstance(wrt, int) else ct
-        got = {w: nan(ct[q]).reshape(()) for q, w in enumerate(bidx)}
+            return self._per_arg(nan(ct), where, wrt, idx)
+        got = {w: nan(ct[q]).reshape(()) if n is None else nan(ct[q:q + n]) for w, (q, n) in where.items()}
         got.update({w: nan(ys[q]) for q, w in enumerate(pidx)})
         return got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx)
 
     def jvp(self, *args, wrt, tangents):
         """forward mode (tallymap's jvp of a mapped call, _api.py:305-345): ONE launch of the generated tangent program.
-        wrt: float32 broadcast argument index or tuple of W indices; tangents: W values (one tangent lane) or an
+        wrt: float32 broadcast argument index or tuple of indices, W scalars in all (a broadcast vector counts its n
+        elements, in order); tangents: W values (one tangent lane) or an
         array [L, W] (L <= 16 lanes, the reference's dual lanes).  -> (Result, {output name: tangent}), a tangent of
         shape (*output.shape) for one lane, (L, *output.shape) for L lanes; NaN when an item hit max_steps."""
         from . import lower
@@ -491,11 +530,11 @@ class MappedFn:
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
         if any(self.in_axes[w] is not None for w in idx):
             raise ValueError("tallymap_b200: tangents of per-item operands are not lowered")
-        bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
+        bpos, _ = self._bleaves(L_, idx)
         tan = torch.as_tensor(np.asarray(tangents, np.float32) if not isinstance(tangents, torch.Tensor)
                               else tangents, dtype=torch.float32)
         lanes_given = tan.dim() == 2
-        tan = tan.reshape(-1, len(idx))
+        tan = tan.reshape(-1, len(bpos))
         L = int(tan.shape[0])
         if L > lower.LANES_MAX:
             raise ValueError(f"tallymap_b200: at most {lower.LANES_MAX} tangent lanes per launch")
@@ -525,7 +564,8 @@ class MappedFn:
         """the Jacobian of every float output w.r.t. the broadcast operands `wrt` by forward mode: one lane per
         operand -> {output name: array (W, *output.shape)}"""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
-        _, dts = self.jvp(*args, wrt=idx, tangents=np.eye(len(idx), dtype=np.float32))
+        W = len(self._bleaves(self.lowered(args), idx)[0])
+        _, dts = self.jvp(*args, wrt=idx, tangents=np.eye(W, dtype=np.float32))
         return dts
 
     def value_and_grad(self, *args, wrt, cotangents, exact_order=False):
@@ -539,10 +579,11 @@ class MappedFn:
             L = self.lowered(moved)
             idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
             if all(self.in_axes[w] is None for w in idx):
-                bpos = tuple(sum(1 for ax in self.in_axes[:w] if ax is None) for w in idx)
+                bpos, where = self._bleaves(L, idx)
                 prog = L.vg_program(bpos)
                 if prog is not None:
-                    return self._onepass(L, prog, moved, wrt, cotangents)
+                    res, ct = self._onepass(L, prog, moved, (), cotangents)
+                    return res, self._per_arg(ct, where, wrt, idx)
         return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
 
     def _onepass(self, L, prog, args, wrt, cotangents):
@@ -572,6 +613,7 @@ class MappedFn:
 
 
 OPTIONS = ("cuda_math", "schedule", "min_blocks_per_sm", "xla_batch_size", "rev_checkpoints", "rev_stats")
+BC_VECTOR_MAX = 64      # a broadcast vector of at most this many elements is lowered as that many broadcast scalars
 BACKENDS = ("auto", "xla")
 
 

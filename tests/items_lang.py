@@ -225,3 +225,19 @@ def divided(t, x, key, a):
         return k + 1, x + 0.05 * (2 * u - 1), t
     k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
     return t, k
+
+
+def walk_theta(t, x, key, theta):
+    """the 1-D walk with its parameters as one broadcast vector: theta = (drift weight, step, bias)"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("hist", tl.clip((x * 64).astype(tl.int32), 0, 63), theta[0] * x + theta[2])
+        return k + 1, x + theta[1] * (2 * u - 1), t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    return t, k
+
+
+def walk_theta_scalars(t, x, key, w, step, bias):
+    """walk_theta with its three parameters as separate broadcast scalars"""
+    return walk_theta(t, x, key, (w, step, bias))

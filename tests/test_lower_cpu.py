@@ -428,3 +428,27 @@ def test_error_types():
         T.trace_item(nested, ["f32"], 1, specs)
     assert isinstance(e.value, NotImplementedError) and isinstance(e.value, T.TraceError)
     assert issubclass(lower.LowerError, tm.UnsupportedError)
+
+
+def test_broadcast_vector_operands():
+    """a broadcast float32[n] operand (n <= 64) is lowered as n broadcast scalars: the item sees a tuple; grad, jvp
+    and value_and_grad address it as one argument (its gradient f32[n])"""
+    from items_lang import walk_theta, walk_theta_scalars
+    outs = {"hist": tm.Sum((64,))}
+    x, k, _ = _args_walk()
+    f = tm.vmap(walk_theta, outputs=outs, in_axes=(0, 0, None), max_steps=1000)
+    g = tm.vmap(walk_theta_scalars, outputs=outs, in_axes=(0, 0, None, None, None), max_steps=1000)
+    th = np.float32([0.5, 0.03, 0.1])
+    L = f.lowered((x, k, th))
+    Ls = g.lowered((x, k, *th))
+    assert L.bc_groups == {2: (0, 3)} and len(L.fwd.bc) == 3
+    assert L.fwd_source.split("struct GenFwd")[1] == Ls.fwd_source.split("struct GenFwd")[1]
+    pi, bc = f._split((x, k, th))
+    assert len(pi) == 2 and len(bc) == 3 and float(bc[1]) == np.float32(0.03)
+    assert f._bleaves(L, (2,)) == ((0, 1, 2), {2: (0, 3)})
+    ct = np.arange(3, dtype=np.float32)
+    assert np.array_equal(f._per_arg(ct, {2: (0, 3)}, 2, (2,)), ct)
+    assert f._per_arg(ct, {3: (0, None), 4: (1, None), 2: (2, None)}, (3, 4, 2), (3, 4, 2)) is ct
+    with pytest.raises(TypeError):
+        f.lowered((x, k, np.zeros(65, np.float32)))
+    assert L.grad_program((0, 1, 2)).kernel > 0

@@ -766,3 +766,27 @@ def test_call_options(cuda):
     g0 = run().grad(x, k, a, wrt=2, cotangents=ct)
     g1 = run(rev_checkpoints=4).grad(x, k, a, wrt=2, cotangents=ct)
     assert near(g1.cpu().numpy(), g0.cpu().numpy())
+
+
+def test_broadcast_vector_operand(cuda):
+    """a broadcast float32[3] parameter vector: the forward, the replay gradient (f32[3]), the one-pass
+    value_and_grad and jacfwd equal those of the same item with three broadcast scalars"""
+    from items_lang import walk_theta, walk_theta_scalars
+    n = 4000
+    x, k = rw_inputs(n, seed=29)
+    th = np.float32([0.5, 0.03, 0.1])
+    outs = {"hist": tm.Sum((64,), fixed_point=True)}
+    f = tm.vmap(walk_theta, outputs=outs, in_axes=(0, 0, None), max_steps=20000)
+    g = tm.vmap(walk_theta_scalars, outputs=outs, in_axes=(0, 0, None, None, None), max_steps=20000)
+    ct = {"hist": torch.linspace(-1, 1, 64)}
+    rf, rg = f(x, k, th), g(x, k, *th)
+    assert np.array_equal(bits(rf.outputs["hist"].cpu().numpy()), bits(rg.outputs["hist"].cpu().numpy()))
+    assert np.array_equal(rf.per_item.cpu().numpy(), rg.per_item.cpu().numpy())
+    gf = f.grad(x, k, th, wrt=2, cotangents=ct)
+    gg = g.grad(x, k, *th, wrt=(2, 3, 4), cotangents=ct)
+    assert gf.shape == (3,) and np.array_equal(bits(gf.cpu().numpy()), bits(gg.cpu().numpy()))
+    _, vf = f.value_and_grad(x, k, th, wrt=2, cotangents=ct)
+    assert vf.shape == (3,) and near(vf.cpu().numpy(), gf.cpu().numpy())
+    J = f.jacfwd(x, k, th, wrt=2)["hist"].cpu().numpy()
+    assert J.shape == (3, 64)
+    assert near(J @ ct["hist"].numpy(), gf.cpu().numpy(), 1e-4)
