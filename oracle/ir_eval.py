@@ -175,6 +175,9 @@ def _eval(e, a):
         return a[1] if a[0] else a[2]
     if p == "inrange":
         return 0 <= a[0] < e.params["n"]
+    if p == "gather":       # a broadcast table's element (the index is clamped into range by the tracer)
+        v = a[0][a[1]]
+        return F32(v) if e.outs[0].dtype == T.F32 else int(v)
     if p == "convert":
         return _convert(a[0], d, e.outs[0].dtype)
     if p == "threefry":
@@ -263,7 +266,10 @@ class Evaluator:
             work[w] = None
             w += 1
             for x, v in zip(tr.inputs[tr.n_per_item:], bc):
-                env[x.id] = F32(v) if x.dtype == T.F32 else int(v)
+                if isinstance(x, T.Table):
+                    env[x.var.id] = np.asarray(v, np.float32 if x.dtype == T.F32 else np.int64).reshape(-1)
+                else:
+                    env[x.id] = F32(v) if x.dtype == T.F32 else int(v)
             out = {"emits": [], "appends": [], "spawns": []}
             self._run_eqns(tr.pre, env, out)
             carry = [self._val(x, env) for x in tr.carry_in]

@@ -384,8 +384,10 @@ class MappedFn:
             return "key"                      # uint32[N, 2] key data (int32 bits on torch)
         if per_item and len(shape) == 1 and dt == "f32":
             return ("f32", shape[0])
-        if not per_item and len(shape) == 1 and dt in ("f32", "i32") and 1 <= shape[0] <= BC_VECTOR_MAX:
+        if not per_item and len(shape) == 1 and dt == "f32" and 1 <= shape[0] <= BC_VECTOR_MAX:
             return (dt, shape[0])             # a broadcast vector: that many broadcast scalars
+        if not per_item and 1 <= len(shape) <= 2 and dt in ("f32", "i32") and 0 < int(np.prod(shape)) < 2 ** 31:
+            return ("table", dt, shape)       # a broadcast table, read by index (lang: t[i], t[i, j])
         raise TypeError(f"tallymap_b200: operand of {'per-item ' if per_item else ''}shape {shape} and dtype {dt} "
                         "is not lowered")
 
@@ -404,15 +406,16 @@ class MappedFn:
             # a broadcast vector is lowered as consecutive broadcast scalars: argument -> (first, n or None)
             groups, leaves = {}, []
             for i, sp in zip(bargs, bcs):
-                groups[i] = (len(leaves), sp[1] if isinstance(sp, tuple) else None)
-                leaves += [sp[0]] * sp[1] if isinstance(sp, tuple) else [sp]
+                vec = isinstance(sp, tuple) and sp[0] != "table"
+                groups[i] = (len(leaves), sp[1] if vec else None)
+                leaves += [sp[0]] * sp[1] if vec else [sp]
             npi = len(pis)
 
             def item(t, *xs):
                 vals = list(xs[:npi])
                 for i in bargs:
                     f, n = groups[i]
-                    vals.append(xs[npi + f] if n is None else tuple(xs[npi + f:npi + f + n]))
+                    vals.append(xs[npi + f] if n is None else T.Vec(xs[npi + f:npi + f + n]))
                 args_ = [None] * len(vals)
                 for pos, x in zip(perm, vals):
                     args_[pos] = x
@@ -435,7 +438,8 @@ class MappedFn:
         for a, ax in zip(args, self.in_axes):
             if ax is None:
                 t = a if isinstance(a, torch.Tensor) else B._host(a)
-                bc += [t[i] for i in range(t.shape[0])] if t.ndim == 1 else [a]
+                vec = t.ndim == 1 and 1 <= t.shape[0] <= BC_VECTOR_MAX and str(t.dtype).endswith("float32")
+                bc += [t[i] for i in range(t.shape[0])] if vec else [a]
         return pi, bc
 
     def _bleaves(self, L, idx):

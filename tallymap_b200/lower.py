@@ -26,7 +26,7 @@ from . import trace as T
 
 CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
 PRIV_BYTES = 4096        # outputs up to this size are privatised per block in shared memory (kernel.py:300)
-CTYPE = {T.F32: "float", T.I32: "i32", T.U32: "u32", T.BOOL: "bool"}
+CTYPE = {T.F32: "float", T.I32: "i32", T.U32: "u32", T.BOOL: "bool", T.TF32: "const float*", T.TI32: "const i32*"}
 SPAWN_STACK_SHARED = 8   # a lane's private stack entries in shared memory (csrc/tm_spawn.cuh kStackShared)
 TDTYPE = {T.F32: torch.float32, T.I32: torch.int32, T.U32: torch.int32, T.BOOL: torch.uint8}
 
@@ -107,6 +107,8 @@ def c_expr(e, a):
         return f"({a[0]} ? {a[1]} : {a[2]})"
     if p == "inrange":
         return f"((u32)({a[0]}) < {int(e.params['n'])}u)"
+    if p == "gather":   # a broadcast table's element; the index is in range by construction (trace.Table)
+        return f"__ldg(&{a[0]}[{a[1]}])"
     if p == "convert":
         return _convert(d, e.outs[0].dtype, a[0])
     if p == "bits":
@@ -206,10 +208,11 @@ class Item:
         self.exact = set(exact)                 # Sum(fixed_point=True) f32 outputs: exact bins
         self.in_specs = list(in_specs)
         npi = tr.n_per_item
-        self.pi, self.bc = tr.inputs[:npi], tr.inputs[npi:]
+        self.pi = tr.inputs[:npi]
+        self.bc = [b.var if isinstance(b, T.Table) else b for b in tr.inputs[npi:]]
         for b in self.bc:
             if not isinstance(b, T.Var):
-                raise LowerError("tallymap_b200.lower: broadcast operands are scalars")
+                raise LowerError("tallymap_b200.lower: broadcast operands are scalars, vectors or tables")
         if any(e.prim == "emit" for e in tr.cond):
             raise LowerError("tallymap_b200.lower: the loop condition may not emit")
         self.specs = list(tr.specs.items())     # [(name, (shape, dtype))]
@@ -252,6 +255,13 @@ class Item:
             self.vars[b.id] = b
         for v in tr.carry + tr.post_carry:
             self.vars[v.id] = v
+
+
+def _bc_setup(k, b):
+    """setup's line for broadcast operand k: a scalar is read once into the context, a table keeps its pointer"""
+    if b.dtype in T.TABLE_ELT:
+        return f"    c.b{k} = static_cast<{CTYPE[b.dtype]}>(P.p[kBc{k}]);"
+    return f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));"
 
 
 def _names_pre(it):
@@ -372,7 +382,7 @@ def forward_source(it, standalone=True):
     for j, s in enumerate(it.in_specs[:npi]):
         ctx.append(f"    const {_in_ctype(s)}* in{j};")
     for k, b in enumerate(it.bc):
-        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")       # (a table: its pointer)
     ctx.append("    i32 M;")
     ctx.append("    i32* stats;")
     tinfo = {}
@@ -412,7 +422,7 @@ def forward_source(it, standalone=True):
     for j, s in enumerate(it.in_specs[:npi]):
         lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
     for k, b in enumerate(it.bc):
-        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+        lines.append(_bc_setup(k, b))
     lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
     lines.append("    c.stats = static_cast<i32*>(P.p[kStats]);")
     for name, (t, S, dt, pv) in tinfo.items():
@@ -664,7 +674,8 @@ def _active(it, wrt, extra=()):
 
     def prop(eqns):
         for e in eqns:
-            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop") or not e.outs:
+            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop", "gather") \
+                    or not e.outs:
                 continue
             if any(isinstance(x, T.Var) and x.id in act for x in e.ins):
                 for o in e.outs:
@@ -763,7 +774,7 @@ class _Rev:
         elif p == "convert":
             if x[0].dtype == T.F32 and e.outs[0].dtype == T.F32:
                 self.add(x[0], g)
-        elif p in ("floor", "round", "stop"):
+        elif p in ("floor", "round", "stop", "gather"):
             pass
         elif p == "rem":
             # lax.rem's transpose (jax: d/dx = 1, d/dy = -sign(x / y) * floor(|x / y|))
@@ -835,7 +846,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     for j, s in enumerate(it.in_specs[:npi]):
         ctx.append(f"    const {_in_ctype(s)}* in{j};")
     for k, b in enumerate(it.bc):
-        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")       # (a table: its pointer)
     ctx += ["    i32 M;", "    i32* stats;", "    u64* gw;", "    float* g;", "    uint8_t* trunc;"]
     ctx += [f"    float* gpi{q};" for q in range(len(pl))]
     ctx += ctx_ct
@@ -877,7 +888,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     for j, s in enumerate(it.in_specs[:npi]):
         lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
     for k, b in enumerate(it.bc):
-        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+        lines.append(_bc_setup(k, b))
     lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
     lines += ["    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.gw = static_cast<u64*>(P.p[kExact]);",
               "    c.g = static_cast<float*>(P.p[kG]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
@@ -1078,6 +1089,8 @@ def _operand(name, spec):
     from .backend import Operand
     if spec == "key":
         return Operand(name, (2,), torch.int32)
+    if isinstance(spec, tuple) and spec[0] == "table":
+        return Operand(name, tuple(spec[2]), TDTYPE[spec[1]])
     if isinstance(spec, tuple):
         return Operand(name, (spec[1],), TDTYPE[spec[0]])
     return Operand(name, (), TDTYPE[spec])
@@ -1126,6 +1139,13 @@ class Lowered:
         self.jvps = {}
         self.vgs = {}
 
+    def _differentiable(self, wrt):
+        """a table is read-only data of the item: no cotangent or tangent flows to it"""
+        for k in wrt:
+            if self.it.bc[k].dtype in T.TABLE_ELT:
+                raise LowerError("tallymap_b200.lower: derivatives with respect to a broadcast table are not lowered "
+                                 "(pass the differentiated parameters as scalars or a vector of at most 64)")
+
     def _compile(self, src, note, nbuf, smem):
         """compile one of this item's programs with the call's options (cuda_math, min_blocks_per_sm)"""
         return compile_kernel(self.head + src, note, nbuf, smem, self.flags)
@@ -1133,6 +1153,7 @@ class Lowered:
     def jvp_program(self, wrt, lanes):
         """the forward-mode program: the forward's outputs and, per tangent lane, the tangents of its float tallies
         for tangents of bc[wrt] given per launch (an input f32[lanes, len(wrt)])"""
+        self._differentiable(wrt)
         from .backend import ItemProgram, TSpec, Operand
         key = (tuple(wrt), int(lanes))
         if key not in self.jvps:
@@ -1167,6 +1188,7 @@ class Lowered:
         active carry the step VJPs summed as the forward runs (OnePassVG); otherwise, for up to FWD_GRAD_MAX
         operands and no fixed-point output, forward mode with the tangents contracted at each emit
         (jvp_source(contract=True)); else None (the replay)"""
+        self._differentiable(wrt)
         from .backend import ItemProgram, TSpec, Operand
         wrt = tuple(wrt)
         if wrt not in self.vgs:
@@ -1202,6 +1224,7 @@ class Lowered:
         """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands) and, per
         item, d <ct, outputs> / d pi[wrt_pi] (positions among the per-item operands: per-item results before the
         truncation flag)"""
+        self._differentiable(wrt)
         from .backend import ItemProgram, TSpec
         wrt, wrt_pi = tuple(wrt), tuple(wrt_pi)
         if self.fwd.records:
@@ -1286,7 +1309,7 @@ def _jvp_rule(e, a, d, out):
         return f"({a[0]} ? {db or '0.0f'} : {dc or '0.0f'})"
     if p == "convert":
         return x if e.outs[0].dtype == T.F32 and e.ins[0].dtype == T.F32 else None
-    if p in ("floor", "round", "stop"):
+    if p in ("floor", "round", "stop", "gather"):
         return None
     if p == "rem":
         q = f"tm_fdiv({a[0]}, {a[1]})"
@@ -1424,7 +1447,7 @@ def jvp_source(it, wrt, L, contract=False):
     for j, s in enumerate(it.in_specs[:npi]):
         ctx.append(f"    const {_in_ctype(s)}* in{j};")
     for k, b in enumerate(it.bc):
-        ctx.append(f"    {CTYPE[b.dtype]} b{k};")
+        ctx.append(f"    {CTYPE[b.dtype]} b{k};")       # (a table: its pointer)
     for q, k in enumerate(wrt):
         for l in range(L):
             ctx.append(f"    float db{k}_{l};")
@@ -1480,7 +1503,7 @@ def jvp_source(it, wrt, L, contract=False):
     for j, s in enumerate(it.in_specs[:npi]):
         lines.append(f"    c.in{j} = static_cast<const {_in_ctype(s)}*>(P.p[kIn{j}]);")
     for k, b in enumerate(it.bc):
-        lines.append(f"    c.b{k} = __ldg(static_cast<const {CTYPE[b.dtype]}*>(P.p[kBc{k}]));")
+        lines.append(_bc_setup(k, b))
     for q, k in enumerate(wrt):
         for l in range(L):
             if contract:

@@ -18,6 +18,8 @@ import dataclasses
 import itertools
 
 F32, I32, U32, BOOL = "f32", "i32", "u32", "bool"
+TF32, TI32 = "tf32", "ti32"          # a broadcast table of float32 / int32 (read by gather)
+TABLE_ELT = {TF32: F32, TI32: I32}
 _CTX = []
 
 
@@ -232,6 +234,78 @@ class Key:
 
     def __init__(self, a, b):
         self.a, self.b = a, b
+
+
+class Vec(tuple):
+    """a per-item or broadcast float32 vector: a tuple of traced scalars that a traced int32 index also reads
+    (jax.numpy's semantics: a negative index counts from the end, then the index is clamped into range), as a chain
+    of selects, so the element read stays differentiable"""
+
+    def __getitem__(self, i):
+        if isinstance(i, (int, slice)) and not isinstance(i, bool):
+            r = tuple.__getitem__(self, i)
+            return Vec(r) if isinstance(i, slice) else r
+        i = _lit(i)
+        if not isinstance(i, Var) or i.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: a vector index is an integer")
+        from . import lang
+        n = len(self)
+        ii = lang.minimum(i, n - 1).astype(I32) if i.dtype == U32 else \
+            lang.clip(lang.where(i < 0, i + n, i), 0, n - 1)
+        r = tuple.__getitem__(self, 0)
+        for j in range(1, n):
+            r = lang.where(ii == j, tuple.__getitem__(self, j), r)
+        return r
+
+
+class Table:
+    """a broadcast array of float32 or int32, shape (n,) or (n, m), read-only in the item: t[i] (a 1-D table's
+    element; a 2-D table's row i as a tuple of m values) and t[i, j], with jax.numpy's indexing semantics for a
+    traced index (a negative index counts from the end, then the index is clamped into range: XLA's gather start
+    index clamp, backends/kernel/op_table.py:1085-1146); a Python int index out of range raises IndexError"""
+    __slots__ = ("var", "shape")
+
+    def __init__(self, var, shape):
+        self.var, self.shape = var, tuple(int(d) for d in shape)
+
+    def __len__(self):
+        return self.shape[0]
+
+    @property
+    def dtype(self):
+        return TABLE_ELT[self.var.dtype]
+
+    def _index(self, i, n):
+        """a Python int (static) or a traced int32 index in [0, n)"""
+        if isinstance(i, bool):
+            raise TraceError("tallymap_b200.lang: a table index is an integer")
+        if isinstance(i, int):
+            if not -n <= i < n:
+                raise IndexError(f"tallymap_b200.lang: index {i} is out of bounds for a table axis of size {n}")
+            return i % n
+        i = _lit(i)
+        if not isinstance(i, Var) or i.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: a table index is an integer")
+        from . import lang
+        if i.dtype == U32:
+            return lang.minimum(i, n - 1).astype(I32)
+        return lang.clip(lang.where(i < 0, i + n, i), 0, n - 1)
+
+    def _gather(self, flat):
+        size = self.shape[0] * (self.shape[1] if len(self.shape) > 1 else 1)
+        return _cur().emit("gather", [self.var, _lit(flat)], [self.dtype], n=size)[0]
+
+    def __getitem__(self, idx):
+        idx = idx if isinstance(idx, tuple) else (idx,)
+        if len(idx) > len(self.shape) or not idx:
+            raise TraceError(f"tallymap_b200.lang: {len(idx)} indices for a table of shape {self.shape}")
+        ii = [self._index(i, n) for i, n in zip(idx, self.shape)]
+        if len(self.shape) == 1:
+            return self._gather(ii[0])
+        row = ii[0] * self.shape[1]
+        if len(ii) == 2:
+            return self._gather(row + ii[1])
+        return tuple(self._gather(row + j) for j in range(self.shape[1]))
 
 
 class TallyToken:
@@ -458,8 +532,10 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
     for s in in_specs:
         if s == "key":
             args.append(Key(tr.new(U32), tr.new(U32)))
+        elif isinstance(s, tuple) and s[0] == "table":
+            args.append(Table(tr.new({F32: TF32, I32: TI32}[s[1]]), s[2]))
         elif isinstance(s, tuple):
-            args.append(tuple(tr.new(s[0]) for _ in range(s[1])))
+            args.append(Vec(tr.new(s[0]) for _ in range(s[1])))
         else:
             args.append(tr.new(s))
     tok = TallyToken(specs, records, list(in_specs[:n_per_item]) if spawn else None)

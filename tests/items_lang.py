@@ -241,3 +241,47 @@ def walk_theta(t, x, key, theta):
 def walk_theta_scalars(t, x, key, w, step, bias):
     """walk_theta with its three parameters as separate broadcast scalars"""
     return walk_theta(t, x, key, (w, step, bias))
+
+
+def lookup(t, x, key, xs, pairs, a):
+    """a walk reading its step size from a 1-D table and a pair of values from a 2-D (n, 2) table, by traced
+    indices that leave the tables' range (clamped) and go negative (counted from the end, then clamped)"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        b = (x * 100).astype(tl.int32)
+        sig = xs[b]
+        lo, hi = pairs[b - 3]
+        t = t.add("h", tl.clip(b // 8, 0, 15), a * sig * (hi - lo))
+        return k + 1, x + 0.05 * (2 * u - 1) * sig, t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    return t, k, xs[-1] + pairs[k, 1]
+
+
+def neighbours(t, i, order, start, pos, theta):
+    """ONE particle of a cell list (a square box of side 8 in 4 x 4 cells, periodic): visit the members of the 3 x 3
+    cells around particle i, one per loop step, summing a pair energy theta[0] * exp(-r^2 / theta[1]) over those
+    within distance 2; tally half of it by the particle's column and return its neighbour count and energy"""
+    xi, yi = pos[i]
+    cx = tl.clip((xi / 2.0).astype(tl.int32), 0, 3)
+    cy = tl.clip((yi / 2.0).astype(tl.int32), 0, 3)
+
+    def body(c):
+        g, p, nb, u, t = c
+        cid = ((cy + g // 3 + 3) % 4) * 4 + (cx + g % 3 + 3) % 4
+        lo, hi = start[cid], start[cid + 1]
+        p = tl.maximum(p, lo)
+        inside = p < hi
+        j = order[p]
+        xj, yj = pos[j]
+        dx = tl.rem(xj - xi + 12.0, 8.0) - 4.0
+        dy = tl.rem(yj - yi + 12.0, 8.0) - 4.0
+        r2 = dx * dx + dy * dy
+        near = inside & (j != i) & (r2 < 4.0)
+        e = tl.where(near, theta[0] * tl.exp(-r2 / theta[1]), 0.0)
+        nxt = p + 1
+        done = ~(nxt < hi)
+        return g + done.astype(tl.int32), tl.where(done, 0, nxt), nb + near.astype(tl.int32), u + e, t
+    g, p, nb, u, t = tl.while_loop(lambda c: c[0] < 9, body, (0, 0, 0, 0.0, t))
+    t = t.add("u", cx, 0.5 * u)
+    return t, nb, u

@@ -449,6 +449,62 @@ def test_broadcast_vector_operands():
     ct = np.arange(3, dtype=np.float32)
     assert np.array_equal(f._per_arg(ct, {2: (0, 3)}, 2, (2,)), ct)
     assert f._per_arg(ct, {3: (0, None), 4: (1, None), 2: (2, None)}, (3, 4, 2), (3, 4, 2)) is ct
-    with pytest.raises(TypeError):
-        f.lowered((x, k, np.zeros(65, np.float32)))
     assert L.grad_program((0, 1, 2)).kernel > 0
+    big = (x, k, np.zeros(65, np.float32))           # past 64 elements: a table, read by index, not differentiable
+    Lb = f.lowered(big)
+    assert Lb.bc_groups == {2: (0, None)} and Lb.fwd.bc[0].shape == (65,)
+    with pytest.raises(tm.UnsupportedError):
+        Lb.grad_program((0,))
+
+
+def test_broadcast_tables():
+    """a broadcast array larger than a parameter vector (or any int32 array, or a 2-D array) is a table read by
+    traced indices with jax.numpy's semantics (negative counts from the end, then clamped); the IR evaluator agrees
+    with numpy's clip-mode take; derivatives with respect to a table raise UnsupportedError"""
+    from items_lang import lookup, neighbours
+    from oracle.ir_eval import Evaluator
+    rng = np.random.default_rng(0)
+    x, k, _ = _args_walk(64)
+    xs = rng.uniform(0.5, 1.5, 100).astype(np.float32)
+    pairs = rng.uniform(-1, 1, (100, 2)).astype(np.float32)
+    f = tm.vmap(lookup, outputs={"h": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None, None, None),
+                max_steps=20000)
+    L = f.lowered((x, k, xs, pairs, np.float32(0.7)))
+    assert [o.shape for o in L.fwd.bc] == [(100,), (100, 2), ()]
+    assert "__ldg(&c.b0[" in L.fwd_source and "__ldg(&c.b1[" in L.fwd_source
+    assert L.grad_program((2,)).kernel > 0 and L.grad_program((), (0,)).kernel > 0
+    with pytest.raises(tm.UnsupportedError):
+        L.grad_program((0,))
+    with pytest.raises(tm.UnsupportedError):
+        L.jvp_program((1,), 1)
+    ref = Evaluator(L.tr, 20000, ("h",)).run([x, k], [xs, pairs, np.float32(0.7)])
+    kk = ref["results"][0]
+    assert np.array_equal(ref["results"][1], xs[-1] + pairs[np.clip(kk, 0, 99), 1])
+    # the cell-list item: neighbour counts equal a brute-force count
+    N = 128
+    pos = rng.uniform(0, 8, (N, 2)).astype(np.float32)
+    cell = np.clip((pos[:, 1] / 2).astype(int), 0, 3) * 4 + np.clip((pos[:, 0] / 2).astype(int), 0, 3)
+    order = np.argsort(cell, kind="stable").astype(np.int32)
+    start = np.searchsorted(cell[order], np.arange(17)).astype(np.int32)
+    g = tm.vmap(neighbours, outputs={"u": tm.Sum((4,))}, in_axes=(0, None, None, None, None), max_steps=1 << 14)
+    ii = np.arange(N, dtype=np.int32)
+    L2 = g.lowered((ii, order, start, pos, np.float32([1.0, 0.5])))
+    assert L2.bc_groups[4] == (3, 2) and [o.shape for o in L2.fwd.bc][:3] == [(N,), (17,), (N, 2)]
+    r = Evaluator(L2.tr, 1 << 14).run([ii], [order, start, pos, 1.0, 0.5])
+    d = (pos[:, None, :] - pos[None, :, :] + 12.0) % 8.0 - 4.0
+    nb = (((d ** 2).sum(-1) < 4.0) & ~np.eye(N, dtype=bool)).sum(1)
+    assert np.array_equal(r["results"][0], nb)
+
+
+def test_vector_traced_index():
+    """a float32 vector read by a traced index: a chain of selects (differentiable), the index wrapped and clamped"""
+    def item(t, p, key, a):
+        i = (a * 10).astype(tl.int32) - 2
+        return t.add("h", 0, p[i] + p[-1]), p[i]
+    tr = T.trace_item(item, [("f32", 3), "key", "f32"], 2, {"h": ((1,), "f32")})
+    from oracle.ir_eval import Evaluator
+    p = np.float32([[1, 2, 3], [4, 5, 6]])
+    keys = prng.split(prng.PRNGKey(0), 2)
+    for a, want in ((0.0, [2, 5]), (0.25, [1, 4]), (0.35, [2, 5]), (0.99, [3, 6]), (-1.0, [1, 4])):
+        r = Evaluator(tr, 10).run([p, keys], [np.float32(a)])
+        assert list(r["results"][0]) == want, (a, r["results"][0])

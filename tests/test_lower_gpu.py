@@ -790,3 +790,46 @@ def test_broadcast_vector_operand(cuda):
     J = f.jacfwd(x, k, th, wrt=2)["hist"].cpu().numpy()
     assert J.shape == (3, 64)
     assert near(J @ ct["hist"].numpy(), gf.cpu().numpy(), 1e-4)
+
+
+def test_broadcast_tables(cuda):
+    """items reading broadcast tables by traced indices (1-D and 2-D, float32 and int32, indices clamped and
+    counted from the end): a lookup walk and a cell-list neighbour item bitwise against the IR evaluator (per-item
+    results and fixed-point tallies); the neighbour energy's gradient w.r.t. its parameter vector (replay and one
+    launch) against jacfwd"""
+    from items_lang import lookup, neighbours
+    from oracle.ir_eval import Evaluator
+    rng = np.random.default_rng(5)
+    n = 300
+    x, k = rw_inputs(n, seed=31)
+    xs = rng.uniform(0.5, 1.5, 100).astype(np.float32)
+    pairs = rng.uniform(-1, 1, (100, 2)).astype(np.float32)
+    f = tm.vmap(lookup, outputs={"h": tm.Sum((16,), fixed_point=True)}, in_axes=(0, 0, None, None, None),
+                max_steps=20000)
+    r = f(x, k, xs, pairs, np.float32(0.7))
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    ref = Evaluator(f.last_lowered.tr, 20000, ("h",)).run([x, k], [xs, pairs, np.float32(0.7)])
+    assert np.array_equal(bits(r.outputs["h"].cpu().numpy()), bits(ref["sums"]["h"]))
+    assert np.array_equal(r.per_item[0].cpu().numpy(), ref["results"][0])
+    assert np.array_equal(bits(r.per_item[1].cpu().numpy()), bits(ref["results"][1]))
+    N = 512
+    pos = rng.uniform(0, 8, (N, 2)).astype(np.float32)
+    cell = np.clip((pos[:, 1] / 2).astype(int), 0, 3) * 4 + np.clip((pos[:, 0] / 2).astype(int), 0, 3)
+    order = np.argsort(cell, kind="stable").astype(np.int32)
+    start = np.searchsorted(cell[order], np.arange(17)).astype(np.int32)
+    th = np.float32([1.0, 0.5])
+    ii = np.arange(N, dtype=np.int32)
+    g = tm.vmap(neighbours, outputs={"u": tm.Sum((4,), fixed_point=True)}, in_axes=(0, None, None, None, None),
+                max_steps=1 << 14)
+    r2 = g(ii, order, start, pos, th)
+    ref2 = Evaluator(g.last_lowered.tr, 1 << 14, ("u",)).run([ii], [order, start, pos, *th])
+    assert np.array_equal(r2.per_item[0].cpu().numpy(), ref2["results"][0])
+    assert np.array_equal(bits(r2.per_item[1].cpu().numpy()), bits(ref2["results"][1]))
+    assert np.array_equal(bits(r2.outputs["u"].cpu().numpy()), bits(ref2["sums"]["u"]))
+    ct = {"u": torch.tensor([1.0, -0.5, 0.25, 2.0])}
+    gr = g.grad(ii, order, start, pos, th, wrt=4, cotangents=ct)
+    _, gv = g.value_and_grad(ii, order, start, pos, th, wrt=4, cotangents=ct)
+    J = g.jacfwd(ii, order, start, pos, th, wrt=4)["u"].cpu().numpy()
+    assert gr.shape == (2,) and near(gr.cpu().numpy(), J @ ct["u"].numpy(), 1e-4)
+    assert near(gv.cpu().numpy(), gr.cpu().numpy(), 1e-4)
