@@ -135,7 +135,9 @@ int tm_tree_generations(void* stream, const void* records, int64_t n_records, in
  * (No counterpart in the reference, which reports no rooflines.) */
 int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used);
 
-/* The backend's f32 math on the device, elementwise: fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y) (y only for pow).
+/* The backend's f32 math on the device, elementwise: fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y), 5 atan,
+ * 6 atan2(x, y) (x the ordinate), 7 asin, 8 acos, 9 tan, 10 sinh, 11 cosh, 12 asinh, 13 acosh, 14 atanh, 15 exp2,
+ * 16 log2, 17 cbrt, 18 erf, 19 erfc, 20 erfinv (y read only by pow and atan2).
  * The item programs use this math on the device and the same code on the host, so the two agree bitwise; this entry
  * point lets a caller check that.  (The reference has no counterpart: its device math is libdevice, its host math
  * libm, backends/kernel/kernel.py:29-57, host.py:9-11.) */

@@ -29,7 +29,8 @@ from tallymap_b200 import trace as T
 from . import oracle as orc
 
 F32 = np.float32
-_MATH = {"log": "log", "exp": "exp", "sin": "sin", "cos": "cos"}
+_MATH = {p: p for p in ("log", "exp", "sin", "cos", "atan", "asin", "acos", "tan", "sinh", "cosh", "asinh", "acosh",
+                         "atanh", "exp2", "log2", "cbrt", "erf", "erfc", "erfinv")}
 
 
 def _wrap32(v):
@@ -151,8 +152,8 @@ def _eval(e, a):
         return (-1 if a[0] < 0 else 0) if sh >= 32 else a[0] >> sh
     if p in _MATH:
         return F32(orc.math(_MATH[p], np.array([a[0]], np.float32))[0])
-    if p == "pow":
-        return F32(orc.math("pow", np.array([a[0]], np.float32), np.array([a[1]], np.float32))[0])
+    if p in ("pow", "atan2"):
+        return F32(orc.math(p, np.array([a[0]], np.float32), np.array([a[1]], np.float32))[0])
     if p == "sqrt":
         with np.errstate(all="ignore"):
             return F32(np.sqrt(F32(a[0])))

@@ -40,6 +40,7 @@ def build(force=False):
     """compile the oracle for this host's CPU (make; a few seconds) -> path of the .so."""
     path = lib_path()
     srcs = [os.path.join(HERE, f) for f in os.listdir(HERE) if f.endswith((".cpp", ".h"))]
+    srcs.append(os.path.join(HERE, "..", "tallymap_b200", "csrc", "tm_math.h"))     # (the shared math it includes)
     if not force and os.path.exists(path) and all(os.path.getmtime(s) <= os.path.getmtime(path) for s in srcs):
         return path
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
@@ -206,7 +207,9 @@ def ph_grad(keys, mu_a=0.1, mu_s=10.0, ct=None, max_steps=100000, C=16, nthreads
     return dict(g=g, trunc=tr.astype(bool), stats=st)
 
 
-MATH_FN = {"log": 0, "exp": 1, "sin": 2, "cos": 3, "pow": 4}
+MATH_FN = {"log": 0, "exp": 1, "sin": 2, "cos": 3, "pow": 4, "atan": 5, "atan2": 6, "asin": 7, "acos": 8, "tan": 9,
+           "sinh": 10, "cosh": 11, "asinh": 12, "acosh": 13, "atanh": 14, "exp2": 15, "log2": 16, "cbrt": 17,
+           "erf": 18, "erfc": 19, "erfinv": 20}
 
 
 def math(fn, x, y=None):

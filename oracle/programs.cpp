@@ -861,15 +861,7 @@ int or_ph_grad(i64 n, const u32* keys, float mu_a, float mu_s, const float* ct, 
 
 // the shared math on the host, elementwise (fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y))
 void or_math(int fn, const float* x, const float* y, float* out, i64 n) {
-  for (i64 i = 0; i < n; ++i) {
-    switch (fn) {
-      case 0: out[i] = tmm::logf(x[i]); break;
-      case 1: out[i] = tmm::expf(x[i]); break;
-      case 2: out[i] = tmm::sinf(x[i]); break;
-      case 3: out[i] = tmm::cosf(x[i]); break;
-      default: out[i] = tmm::powf(x[i], y[i]); break;
-    }
-  }
+  for (i64 i = 0; i < n; ++i) out[i] = tmm::eval(fn, x[i], y ? y[i] : 0.0f);
 }
 
 int or_od_fwd(i64 n, const float* sigma, const float* rho, const float* y0, const i32* id, float beta, i32 max_steps,

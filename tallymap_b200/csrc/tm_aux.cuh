@@ -156,16 +156,7 @@ __global__ void tree_scatter_kernel(const unsigned char* rec, long long n, int s
 
 __global__ void math_eval_kernel(int fn, const float* x, const float* y, float* out, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float a = x[i];
-    float r;
-    switch (fn) {
-      case 0: r = tmm::logf(a); break;
-      case 1: r = tmm::expf(a); break;
-      case 2: r = tmm::sinf(a); break;
-      case 3: r = tmm::cosf(a); break;
-      default: r = tmm::powf(a, y[i]); break;
-    }
-    out[i] = r;
+    out[i] = tmm::eval(fn, x[i], y ? y[i] : 0.0f);
   }
 }
 

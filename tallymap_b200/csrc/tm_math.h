@@ -14,6 +14,18 @@
 //   sin, cos   x = n pi/2 + r by a three-part pi/2 (exact products for |x| < 2^20), |r| <= pi/4; Taylor series of sin and cos
 //         to r^19 / r^20, then the quadrant's sign and swap
 //   pow   x^y = exp(y log x) for x > 0 (the exponent's argument formed in double), IEEE special cases otherwise
+//   atan  |x| > 1: pi/2 - atan(1/x); t > tan(pi/12): pi/6 + atan((t sqrt3 - 1) / (t + sqrt3)); then the odd Taylor
+//         series to t^31 for t <= 0.268 (truncation below 2e-20 relative); atan2 the quadrant of atan(|y| / |x|) and
+//         C's special cases; asin x = atan(x / sqrt((1 - x)(1 + x))), acos x = 2 atan(sqrt((1 - x) / (1 + x)))
+//   tan   the sin / cos reduction above, sin r / cos r or -cos r / sin r by the quadrant's parity
+//   sinh, cosh, asinh, acosh, atanh   their exponential and logarithmic forms, by the Taylor series to x^7 for
+//         |x| < 2^-10 where the forms cancel
+//   exp2, log2   e^(x ln 2) and log x / ln 2; cbrt e^(log|x| / 3) and one Newton step, with the sign of x
+//   erf   |x| < 2: its Maclaurin series (46 terms); erfc, x >= 2: Laplace's continued fraction
+//         erfc x = e^(-x^2) / sqrt(pi) / (x + (1/2) / (x + 1 / (x + (3/2) / (x + ...)))) to depth 60; else 1 - the other
+//   erfinv  five Newton steps on erf (on erfc above 1/2, from 1 - y exact in double), from the series
+//         (sqrt(pi) / 2)(y + pi y^3 / 12 + 7 pi^2 y^5 / 480 + 127 pi^3 y^7 / 40320) for y <= 0.9 and from the
+//         asymptotic x^2 = -log(sqrt(pi) x (1 - y)), iterated three times, above
 #pragma once
 #ifdef __CUDACC_RTC__
 #include <cuda/std/cstdint>
@@ -22,6 +34,7 @@ typedef cuda::std::uint64_t uint64_t;
 typedef cuda::std::int32_t int32_t;
 typedef cuda::std::int64_t int64_t;
 #else
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #endif
@@ -202,6 +215,11 @@ TM_HD void sincosf(float xf, float* s, float* c) {
     *c = f32_nan();
     return;
   }
+  if (xf == 0.0f) {   // sin(-0) = -0
+    *s = xf;
+    *c = 1.0f;
+    return;
+  }
   const double k = x * kTwoOverPi;
   const long long n = (long long)(k < 0.0 ? k - 0.5 : k + 0.5);
   const double dn = (double)n;
@@ -231,5 +249,279 @@ TM_HD float powf(float x, float y) {
   if (a < -104.0) return 0.0f;
   return to_f32(exp_d(a));
 }
+
+constexpr double kPi = 3.14159265358979311600e+00;
+constexpr double kPio2 = 1.57079632679489655800e+00;
+constexpr double kPio4 = 7.85398163397448278999e-01;
+constexpr double kPio6 = 5.23598775598298815658e-01;
+constexpr double kSqrt3 = 1.73205080756887719318e+00;
+constexpr double kTanPio12 = 2.67949192431122695603e-01;   // 2 - sqrt 3
+constexpr double kSqrtPi = 1.77245385090551588192e+00;
+constexpr double kTwoOverSqrtPi = 1.12837916709551255856e+00;
+constexpr double kTiny = 9.765625e-04;                      // 2^-10: below it the odd Taylor forms
+
+TM_HD double sqrt_d(double x) {     // IEEE square root, correctly rounded on both sides
+#if defined(__CUDA_ARCH__)
+  return __dsqrt_rn(x);
+#else
+  return std::sqrt(x);
+#endif
+}
+TM_HD bool sign_(float x) { return (f2u(x) >> 31) != 0u; }
+TM_HD bool isinf_(float x) { return x == f32_inf() || x == -f32_inf(); }
+TM_HD float with_sign(double r, bool neg) { return to_f32(neg ? -r : r); }
+
+// atan t for 0 <= t <= tan(pi/12): sum_k (-1)^k t^(2k+1) / (2k+1), k <= 15
+TM_HD double atan_core(double t) {
+  const double t2 = t * t;
+  double p = -1.0 / 31.0;
+  p = p * t2 + 1.0 / 29.0;
+  p = p * t2 - 1.0 / 27.0;
+  p = p * t2 + 1.0 / 25.0;
+  p = p * t2 - 1.0 / 23.0;
+  p = p * t2 + 1.0 / 21.0;
+  p = p * t2 - 1.0 / 19.0;
+  p = p * t2 + 1.0 / 17.0;
+  p = p * t2 - 1.0 / 15.0;
+  p = p * t2 + 1.0 / 13.0;
+  p = p * t2 - 1.0 / 11.0;
+  p = p * t2 + 1.0 / 9.0;
+  p = p * t2 - 1.0 / 7.0;
+  p = p * t2 + 1.0 / 5.0;
+  p = p * t2 - 1.0 / 3.0;
+  p = p * t2 + 1.0;
+  return t * p;
+}
+TM_HD double atan_unit(double t) {   // 0 <= t <= 1
+  if (t > kTanPio12) return kPio6 + atan_core((t * kSqrt3 - 1.0) / (t + kSqrt3));
+  return atan_core(t);
+}
+TM_HD double atan_d(double x) {      // x >= 0, +inf allowed
+  if (x > 1.0) return kPio2 - atan_unit(1.0 / x);
+  return atan_unit(x);
+}
+
+TM_HD float atanf(float x) {
+  if (isnan_(x) || x == 0.0f) return x;
+  return with_sign(atan_d(sign_(x) ? -(double)x : (double)x), sign_(x));
+}
+
+// C's atan2: the angle of (x, y), with its signed-zero and infinite special cases
+TM_HD float atan2f(float y, float x) {
+  if (isnan_(x) || isnan_(y)) return f32_nan();
+  const bool yn = sign_(y), xn = sign_(x);
+  double r;
+  if (y == 0.0f) {
+    r = xn ? kPi : 0.0;
+  } else if (x == 0.0f) {
+    r = kPio2;
+  } else if (isinf_(y)) {
+    r = isinf_(x) ? (xn ? 3.0 * kPio4 : kPio4) : kPio2;
+  } else if (isinf_(x)) {
+    r = xn ? kPi : 0.0;
+  } else {
+    const double ay = yn ? -(double)y : (double)y, ax = xn ? -(double)x : (double)x;
+    const double a = atan_d(ay / ax);
+    r = xn ? kPi - a : a;
+  }
+  return with_sign(r, yn);
+}
+
+TM_HD float asinf(float x) {
+  if (isnan_(x) || x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  if (a > 1.0) return f32_nan();
+  if (a == 1.0) return with_sign(kPio2, sign_(x));
+  return with_sign(atan_d(a / sqrt_d((1.0 - a) * (1.0 + a))), sign_(x));
+}
+
+TM_HD float acosf(float x) {
+  if (isnan_(x) || x > 1.0f || x < -1.0f) return f32_nan();
+  if (x == 1.0f) return 0.0f;
+  if (x == -1.0f) return to_f32(kPi);
+  const double d = (double)x;
+  return to_f32(2.0 * atan_d(sqrt_d((1.0 - d) / (1.0 + d))));
+}
+
+// tan of an f32 argument with |x| < 2^20 (larger: NaN), by the sin / cos reduction
+TM_HD float tanf(float xf) {
+  const double x = (double)xf;
+  if (isnan_(xf) || !(x < 1048576.0 && x > -1048576.0)) return f32_nan();
+  if (xf == 0.0f) return xf;
+  const double k = x * kTwoOverPi;
+  const long long n = (long long)(k < 0.0 ? k - 0.5 : k + 0.5);
+  const double dn = (double)n;
+  const double r = ((x - dn * kPio2_1) - dn * kPio2_2) - dn * kPio2_3;
+  const double sr = sin_core(r), cr = cos_core(r);
+  return to_f32((n & 1) ? -cr / sr : sr / cr);
+}
+
+TM_HD float sinhf(float x) {
+  if (isnan_(x) || x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  if (a > 200.0) return sign_(x) ? -f32_inf() : f32_inf();
+  double r;
+  if (a < kTiny) {
+    const double a2 = a * a;
+    r = a + a * (a2 * (1.0 / 6.0 + a2 * (1.0 / 120.0 + a2 * (1.0 / 5040.0))));
+  } else {
+    const double e = exp_d(a);
+    r = 0.5 * (e - 1.0 / e);
+  }
+  return with_sign(r, sign_(x));
+}
+
+TM_HD float coshf(float x) {
+  if (isnan_(x)) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  if (a > 200.0) return f32_inf();
+  const double e = exp_d(a);
+  return to_f32(0.5 * (e + 1.0 / e));
+}
+
+TM_HD float asinhf(float x) {
+  if (isnan_(x) || isinf_(x) || x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  double r;
+  if (a < kTiny) {
+    const double a2 = a * a;
+    r = a + a * (a2 * (-1.0 / 6.0 + a2 * (3.0 / 40.0 + a2 * (-5.0 / 112.0))));
+  } else {
+    r = log_pos(a + sqrt_d(a * a + 1.0));
+  }
+  return with_sign(r, sign_(x));
+}
+
+TM_HD float acoshf(float x) {
+  if (isnan_(x) || x < 1.0f) return f32_nan();
+  if (x == f32_inf()) return x;
+  if (x == 1.0f) return 0.0f;
+  const double d = (double)x;
+  return to_f32(log_pos(d + sqrt_d((d - 1.0) * (d + 1.0))));
+}
+
+TM_HD float atanhf(float x) {
+  if (isnan_(x) || x > 1.0f || x < -1.0f) return f32_nan();
+  if (x == 1.0f || x == -1.0f) return x == 1.0f ? f32_inf() : -f32_inf();
+  if (x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  double r;
+  if (a < kTiny) {
+    const double a2 = a * a;
+    r = a + a * (a2 * (1.0 / 3.0 + a2 * (1.0 / 5.0 + a2 * (1.0 / 7.0))));
+  } else {
+    r = 0.5 * log_pos((1.0 + a) / (1.0 - a));
+  }
+  return with_sign(r, sign_(x));
+}
+
+TM_HD float exp2f(float x) {
+  if (isnan_(x)) return x;
+  if (x >= 128.0f) return f32_inf();
+  if (x < -150.0f) return 0.0f;
+  return to_f32(exp_d((double)x * kLn2));
+}
+
+TM_HD float log2f(float x) {
+  if (isnan_(x) || x < 0.0f) return f32_nan();
+  if (x == 0.0f) return -f32_inf();
+  if (x == f32_inf()) return x;
+  return to_f32(log_pos((double)x) / kLn2);
+}
+
+TM_HD float cbrtf(float x) {
+  if (isnan_(x) || isinf_(x) || x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  double r = exp_d(log_pos(a) / 3.0);
+  r = r - (r * r * r - a) / (3.0 * r * r);
+  return with_sign(r, sign_(x));
+}
+
+// erf x for 0 <= x < 2: (2 / sqrt pi) sum_n (-1)^n x^(2n+1) / (n! (2n+1)), n <= 45
+TM_HD double erf_series(double x) {
+  const double x2 = x * x;
+  double term = x, sum = x;
+  for (int n = 1; n <= 45; ++n) {
+    term = term * (-x2) / (double)n;
+    sum = sum + term / (double)(2 * n + 1);
+  }
+  return kTwoOverSqrtPi * sum;
+}
+// erfc x for 2 <= x <= 14: Laplace's continued fraction, evaluated from depth 60 up
+TM_HD double erfc_cf(double x) {
+  double f = 0.0;
+  for (int k = 60; k >= 1; --k) f = ((double)k * 0.5) / (x + f);
+  return exp_d(-x * x) / kSqrtPi / (x + f);
+}
+TM_HD double erfc_pos(double x) {   // x >= 0
+  if (x < 2.0) return 1.0 - erf_series(x);
+  if (x > 14.0) return 0.0;
+  return erfc_cf(x);
+}
+
+TM_HD float erff(float x) {
+  if (isnan_(x) || x == 0.0f) return x;
+  const double a = sign_(x) ? -(double)x : (double)x;
+  const double r = a < 2.0 ? erf_series(a) : 1.0 - erfc_pos(a);
+  return with_sign(r, sign_(x));
+}
+
+TM_HD float erfcf(float x) {
+  if (isnan_(x)) return x;
+  const double d = (double)x;
+  if (d >= 0.0) return to_f32(erfc_pos(d));
+  const double a = -d;
+  return to_f32(a < 2.0 ? 1.0 + erf_series(a) : 2.0 - erfc_pos(a));
+}
+
+// the inverse of erf on (-1, 1); +-1: +-inf; beyond: NaN
+TM_HD float erfinvf(float y) {
+  if (isnan_(y) || y > 1.0f || y < -1.0f) return f32_nan();
+  if (y == 1.0f || y == -1.0f) return y == 1.0f ? f32_inf() : -f32_inf();
+  if (y == 0.0f) return y;
+  const double a = sign_(y) ? -(double)y : (double)y;
+  const double q = 1.0 - a;   // exact: y is an f32
+  double x;
+  if (a <= 0.9) {
+    const double a2 = a * a;
+    x = 0.886226925452758 * a * (1.0 + a2 * (0.2617993877991494 + a2 * (0.14393173084921979 + a2 * 0.09766361950392055)));
+  } else {
+    x = sqrt_d(-log_pos(q * kSqrtPi));
+    for (int i = 0; i < 2; ++i) x = sqrt_d(-log_pos(q * x * kSqrtPi));
+  }
+  for (int i = 0; i < 5; ++i) {
+    const double d = a < 0.5 ? a - erf_series(x) : erfc_pos(x) - q;
+    x = x + d * (kSqrtPi * 0.5) * exp_d(x * x);
+  }
+  return with_sign(x, sign_(y));
+}
+
+// the shared dispatch of tm_math_eval and the oracle's or_math: fn as tallymap_b200.lower MATH_IDS
+TM_HD float eval(int fn, float x, float y) {
+  switch (fn) {
+    case 0: return logf(x);
+    case 1: return expf(x);
+    case 2: return sinf(x);
+    case 3: return cosf(x);
+    case 4: return powf(x, y);
+    case 5: return atanf(x);
+    case 6: return atan2f(x, y);
+    case 7: return asinf(x);
+    case 8: return acosf(x);
+    case 9: return tanf(x);
+    case 10: return sinhf(x);
+    case 11: return coshf(x);
+    case 12: return asinhf(x);
+    case 13: return acoshf(x);
+    case 14: return atanhf(x);
+    case 15: return exp2f(x);
+    case 16: return log2f(x);
+    case 17: return cbrtf(x);
+    case 18: return erff(x);
+    case 19: return erfcf(x);
+    default: return erfinvf(x);
+  }
+}
+constexpr int kMathFns = 21;
 
 }  // namespace tmm

@@ -3,7 +3,9 @@ jax.random and lax.while_loop with jax's semantics, the ones the reference's op 
 (tallymap/backends/kernel/op_table.py: arithmetic, comparisons, select, conversions, transcendentals, threefry,
 random_bits / fold_in / split, while, round, rem, stop_gradient), and compositions of them with jax's semantics
 (clip, sign, square, mod, log1p, expm1, tanh, the reductions sum / max / min / all / any, cumsum and searchsorted
-over a per-item vector, random.bernoulli).
+over a per-item vector, random.bernoulli); the inverse trigonometric, hyperbolic, exp2 / log2 / cbrt and erf / erfc /
+erfinv primitives (random.normal over erfinv as jax.random forms it, random.exponential), ceil, log10, logistic and
+isfinite as jax.numpy forms them.
 
     from tallymap_b200 import lang as tl
 
@@ -62,6 +64,103 @@ def sqrt(x):
 
 def floor(x):
     return _f32("floor", x)
+
+
+def ceil(x):
+    """jnp.ceil: -floor(-x) (exact)"""
+    return -floor(-x)
+
+
+def arctan(x):
+    return _f32("atan", x)
+
+
+def arctan2(y, x):
+    """jnp.arctan2(y, x) (lax.atan2): the angle of (x, y) in (-pi, pi], C's signed-zero and infinite cases"""
+    y0 = y if isinstance(y, T.Var) else None
+    x0 = x if isinstance(x, T.Var) else None
+    y, x = T._lit(y, x0), T._lit(x, y0)
+    if x.dtype != T.F32 or y.dtype != T.F32:
+        raise T.TraceError("tallymap_b200.lang.arctan2 takes float32")
+    return T._cur().emit("atan2", [y, x], [T.F32])[0]
+
+
+def arcsin(x):
+    return _f32("asin", x)
+
+
+def arccos(x):
+    return _f32("acos", x)
+
+
+def tan(x):
+    return _f32("tan", x)
+
+
+def sinh(x):
+    return _f32("sinh", x)
+
+
+def cosh(x):
+    return _f32("cosh", x)
+
+
+def arcsinh(x):
+    return _f32("asinh", x)
+
+
+def arccosh(x):
+    return _f32("acosh", x)
+
+
+def arctanh(x):
+    return _f32("atanh", x)
+
+
+def exp2(x):
+    return _f32("exp2", x)
+
+
+def log2(x):
+    return _f32("log2", x)
+
+
+def log10(x):
+    """jnp.log10: log(x) / log(10) in float32, as jax.numpy forms it"""
+    return log(x) / 2.30258512
+
+
+def cbrt(x):
+    return _f32("cbrt", x)
+
+
+def erf(x):
+    """jax.scipy.special.erf / lax.erf"""
+    return _f32("erf", x)
+
+
+def erfc(x):
+    """jax.scipy.special.erfc / lax.erfc"""
+    return _f32("erfc", x)
+
+
+def erfinv(x):
+    """jax.scipy.special.erfinv / lax.erf_inv: the inverse of erf on (-1, 1), +-inf at +-1"""
+    return _f32("erfinv", x)
+
+
+def logistic(x):
+    """jax.nn.sigmoid / lax.logistic: 1 / (1 + exp(-x))"""
+    return 1.0 / (1.0 + exp(-x))
+
+
+def isfinite(x):
+    """jnp.isfinite: neither infinite nor NaN (x - x is 0 exactly then)"""
+    return (x - x) == 0.0
+
+
+atan, atan2, asin, acos, asinh, acosh, atanh = arctan, arctan2, arcsin, arccos, arcsinh, arccosh, arctanh
+sigmoid = logistic
 
 
 def abs(x):   # noqa: A001 (jnp.abs)
@@ -269,6 +368,20 @@ class random:
         return tuple(v < p for v in u) if isinstance(u, tuple) else u < p
 
     @staticmethod
+    def normal(key, shape=(), dtype=float32):
+        """jax.random.normal: sqrt(2) erf_inv(u) for u = uniform(key, shape, minval=nextafter(-1, 0), maxval=1)"""
+        if dtype != float32:
+            raise T.TraceError("tallymap_b200.lang.random.normal: float32 only")
+        u = random.uniform(key, shape, minval=-0.99999994, maxval=1.0)
+        return tuple(1.41421354 * erfinv(v) for v in u) if isinstance(u, tuple) else 1.41421354 * erfinv(u)
+
+    @staticmethod
+    def exponential(key, shape=(), dtype=float32):
+        """jax.random.exponential: -log1p(-u) for u = uniform(key, shape)"""
+        u = random.uniform(key, shape, dtype)
+        return tuple(-log1p(-v) for v in u) if isinstance(u, tuple) else -log1p(-u)
+
+    @staticmethod
     def uniform(key, shape=(), dtype=float32, minval=0.0, maxval=1.0):
         """jax.random.uniform: the mantissa fill of random bits in [1, 2) minus 1, then max(lo, f * (hi - lo) + lo)"""
         if dtype != float32:
@@ -280,8 +393,12 @@ class random:
             if not (isinstance(minval, float) and isinstance(maxval, float) and minval == 0.0 and maxval == 1.0):
                 # jax computes max(lo, f * (hi - lo) + lo); for lo = 0, hi = 1 that is f itself, bitwise
                 lo, hi = minval, maxval
-                f = maximum(lo, f * (hi - lo) + lo) if isinstance(hi, T.Var) or isinstance(lo, T.Var) \
-                    else maximum(float(lo), f * float(hi - lo) + float(lo))
+                if isinstance(hi, T.Var) or isinstance(lo, T.Var):
+                    f = maximum(lo, f * (hi - lo) + lo)
+                else:           # float32 bounds and their float32 difference, as jax forms them
+                    import numpy as np
+                    lo32, hi32 = np.float32(lo), np.float32(hi)
+                    f = maximum(float(lo32), f * float(np.float32(hi32 - lo32)) + float(lo32))
             out.append(f)
         return out[0] if shape == () else tuple(out)
 

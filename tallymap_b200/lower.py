@@ -54,7 +54,31 @@ def c_lit(lit):
 
 _BIN = {"add": "+", "sub": "-", "mul": "*", "div": "/", "lt": "<", "le": "<=", "gt": ">", "ge": ">=", "eq": "==",
         "ne": "!="}
-_MATH = {"log": "tmm::logf", "exp": "tmm::expf", "sin": "tmm::sinf", "cos": "tmm::cosf"}
+_MATH = {"log": "tmm::logf", "exp": "tmm::expf", "sin": "tmm::sinf", "cos": "tmm::cosf", "atan": "tmm::atanf",
+         "asin": "tmm::asinf", "acos": "tmm::acosf", "tan": "tmm::tanf", "sinh": "tmm::sinhf", "cosh": "tmm::coshf",
+         "asinh": "tmm::asinhf", "acosh": "tmm::acoshf", "atanh": "tmm::atanhf", "exp2": "tmm::exp2f",
+         "log2": "tmm::log2f", "cbrt": "tmm::cbrtf", "erf": "tmm::erff", "erfc": "tmm::erfcf",
+         "erfinv": "tmm::erfinvf"}
+# d out / d x of the unary math primitives above beyond log / exp / sin / cos, as C over the input's and the
+# output's expressions (jax's jvp rules: lax.py atan, asin, acos, tan, sinh, cosh, asinh, acosh, atanh, exp2, log2,
+# cbrt; special.py erf, erfc, erf_inv)
+_DERIV = {
+    "atan": lambda a, o: f"tm_fdiv(1.0f, (1.0f + {a} * {a}))",
+    "asin": lambda a, o: f"tm_fdiv(1.0f, tm_fsqrt((1.0f - {a}) * (1.0f + {a})))",
+    "acos": lambda a, o: f"(-tm_fdiv(1.0f, tm_fsqrt((1.0f - {a}) * (1.0f + {a}))))",
+    "tan": lambda a, o: f"(1.0f + {o} * {o})",
+    "sinh": lambda a, o: f"tmm::coshf({a})",
+    "cosh": lambda a, o: f"tmm::sinhf({a})",
+    "asinh": lambda a, o: f"tm_fdiv(1.0f, tm_fsqrt({a} * {a} + 1.0f))",
+    "acosh": lambda a, o: f"tm_fdiv(1.0f, tm_fsqrt(({a} - 1.0f) * ({a} + 1.0f)))",
+    "atanh": lambda a, o: f"tm_fdiv(1.0f, ((1.0f - {a}) * (1.0f + {a})))",
+    "exp2": lambda a, o: f"({o} * 0.693147182f)",
+    "log2": lambda a, o: f"tm_fdiv(1.0f, ({a} * 0.693147182f))",
+    "cbrt": lambda a, o: f"tm_fdiv(1.0f, (3.0f * ({o} * {o})))",
+    "erf": lambda a, o: f"(1.12837917f * tmm::expf(-({a} * {a})))",
+    "erfc": lambda a, o: f"(-1.12837917f * tmm::expf(-({a} * {a})))",
+    "erfinv": lambda a, o: f"(0.886226925f * tmm::expf({o} * {o}))",
+}
 
 
 def c_expr(e, a):
@@ -85,6 +109,8 @@ def c_expr(e, a):
         return f"((u32)({a[1]}) >= 32u ? ({a[0]} < 0 ? (i32)-1 : (i32)0) : ({a[0]} >> (u32)({a[1]})))"
     if p in _MATH:
         return f"{_MATH[p]}({a[0]})"
+    if p == "atan2":
+        return f"tmm::atan2f({a[0]}, {a[1]})"
     if p == "sqrt":
         return f"tm_fsqrt({a[0]})"
     if p == "floor":
@@ -749,6 +775,12 @@ class _Rev:
             self.add(x[1], f"(((-{g}) * {a[0]}) * tm_fdiv(1.0f, ({a[1]} * {a[1]})))")
         elif p == "neg":
             self.add(x[0], f"(-{g})")
+        elif p in _DERIV:
+            self.add(x[0], f"({g} * {_DERIV[p](a[0], out)})")
+        elif p == "atan2":
+            inv = f"tm_fdiv(1.0f, ({a[0]} * {a[0]} + {a[1]} * {a[1]}))"
+            self.add(x[0], f"(({g} * {a[1]}) * {inv})")
+            self.add(x[1], f"(((-{g}) * {a[0]}) * {inv})")
         elif p == "log":
             self.add(x[0], f"tm_fdiv({g}, {a[0]})")
         elif p == "exp":
@@ -1284,6 +1316,12 @@ def _jvp_rule(e, a, d, out):
                     None if y is None else f"(((-{y}) * {a[0]}) * tm_fdiv(1.0f, ({a[1]} * {a[1]})))")
     if p == "neg":
         return None if x is None else f"(-{x})"
+    if p in _DERIV:
+        return None if x is None else f"({x} * {_DERIV[p](a[0], out)})"
+    if p == "atan2":
+        inv = f"tm_fdiv(1.0f, ({a[0]} * {a[0]} + {a[1]} * {a[1]}))"
+        return plus(None if x is None else f"(({x} * {a[1]}) * {inv})",
+                    None if y is None else f"(((-{y}) * {a[0]}) * {inv})")
     if p == "log":
         return None if x is None else f"tm_fdiv({x}, {a[0]})"
     if p == "exp":

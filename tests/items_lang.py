@@ -285,3 +285,22 @@ def neighbours(t, i, order, start, pos, theta):
     g, p, nb, u, t = tl.while_loop(lambda c: c[0] < 9, body, (0, 0, 0, 0.0, t))
     t = t.add("u", cx, 0.5 * u)
     return t, nb, u
+
+
+def special(t, x, key, a):
+    """every math primitive beyond log / exp / sin / cos, on values inside their domains, with the normal and
+    exponential samplers: the per-item sum is tallied, and returned with a few of the values"""
+    def body(c):
+        k, s, t = c
+        kk = tl.random.fold_in(key, k)
+        z = tl.random.normal(kk)
+        e = tl.random.exponential(tl.random.fold_in(kk, 7))
+        u = tl.random.uniform(tl.random.fold_in(kk, 9), minval=-0.9, maxval=0.9)
+        v = (tl.arctan(a * x + z) + tl.arctan2(z, a + u) + tl.arcsin(u * a * 0.5) + tl.arccos(u) + tl.tan(u)
+             + tl.sinh(u * a) + tl.cosh(u) + tl.arcsinh(z * a) + tl.arccosh(1.5 + e * a) + tl.arctanh(u)
+             + tl.exp2(u * a) + tl.log2(1.0 + e) + tl.cbrt(z * a) + tl.erf(z * a) + tl.erfc(u + a)
+             + tl.erfinv(u * 0.9) + tl.log10(1.0 + e) + tl.logistic(z) + tl.ceil(u * 4.0))
+        t = t.add("h", (tl.clip(u * 4.0 + 4.0, 0.0, 7.0)).astype(tl.int32), v * 0.01)
+        return k + 1, s + v, t
+    k, s, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
+    return t, s, tl.isfinite(s).astype(tl.int32)

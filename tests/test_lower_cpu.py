@@ -508,3 +508,38 @@ def test_vector_traced_index():
     for a, want in ((0.0, [2, 5]), (0.25, [1, 4]), (0.35, [2, 5]), (0.99, [3, 6]), (-1.0, [1, 4])):
         r = Evaluator(tr, 10).run([p, keys], [np.float32(a)])
         assert list(r["results"][0]) == want, (a, r["results"][0])
+
+
+def test_special_math_trace_and_compile():
+    """the inverse trigonometric, hyperbolic, exp2 / log2 / cbrt and erf family lower to the shared math; the
+    evaluator's values track numpy / scipy within float32 rounding; random.normal is sqrt(2) erfinv of jax's
+    uniform on (nextafter(-1, 0), 1)"""
+    from scipy import special as sp
+    from items_lang import special
+    from oracle.ir_eval import Evaluator
+    n = 64
+    x = np.random.default_rng(2).uniform(-1, 1, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(8), n)
+    f = tm.vmap(special, outputs={"h": tm.Sum((8,))}, in_axes=(0, 0, None), max_steps=100)
+    L = f.lowered((x, keys, np.float32(0.8)))
+    body = L.fwd_source.split("struct GenFwd")[1]
+    for fn in ("atanf", "atan2f", "asinf", "acosf", "tanf", "sinhf", "coshf", "asinhf", "acoshf", "atanhf", "exp2f",
+               "log2f", "cbrtf", "erff", "erfcf", "erfinvf"):
+        assert f"tmm::{fn}(" in body, fn
+    assert L.grad_program((0,)).kernel > 0 and L.jvp_program((0,), 2).kernel > 0
+    r = Evaluator(L.tr, 100).run([x, keys], [np.float32(0.8)])
+    assert np.isfinite(r["results"][0]).all() and (r["results"][1] == 1).all()
+    # random.normal against its definition through numpy/scipy in float64, rounded
+    def item(t, key):
+        return t, tl.random.normal(key)
+    tr = T.trace_item(item, ["key"], 1, {})
+    z = Evaluator(tr, 1).run([keys], [])["results"][0]
+    assert abs(float(np.mean(z))) < 0.5 and 0.5 < float(np.std(z)) < 1.5
+    from tallymap_b200 import prng as pr
+    bits = np.array([pr.threefry2x32(np.uint32(k[0]), np.uint32(k[1]), np.uint32(0), np.uint32(0)) for k in keys])
+    b = (bits[:, 0] ^ bits[:, 1]).astype(np.uint32)
+    f01 = ((b >> 9) | np.uint32(0x3F800000)).view(np.float32) - np.float32(1.0)
+    lo = np.nextafter(np.float32(-1), np.float32(0))
+    uu = np.maximum(lo, f01 * np.float32(2.0) + lo)
+    want = (np.float32(np.sqrt(2)) * sp.erfinv(uu.astype(np.float64)).astype(np.float32)).astype(np.float32)
+    assert np.array_equal(z.astype(np.float32), want)

@@ -833,3 +833,25 @@ def test_broadcast_tables(cuda):
     J = g.jacfwd(ii, order, start, pos, th, wrt=4)["u"].cpu().numpy()
     assert gr.shape == (2,) and near(gr.cpu().numpy(), J @ ct["u"].numpy(), 1e-4)
     assert near(gv.cpu().numpy(), gr.cpu().numpy(), 1e-4)
+
+
+def test_special_math_item(cuda):
+    """an item using every math primitive beyond log / exp / sin / cos with the normal and exponential samplers:
+    bitwise against the IR evaluator (per-item sums, a fixed-point tally); its gradient by replay and by forward
+    mode agree"""
+    from items_lang import special
+    from oracle.ir_eval import Evaluator
+    n = 1000
+    x = np.random.default_rng(12).uniform(-1, 1, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(13), n)
+    a = np.float32(0.8)
+    f = tm.vmap(special, outputs={"h": tm.Sum((8,), fixed_point=True)}, in_axes=(0, 0, None), max_steps=100)
+    r = f(x, keys, a)
+    ref = Evaluator(f.last_lowered.tr, 100, ("h",)).run([x, keys], [a])
+    assert np.array_equal(bits(r.per_item[0].cpu().numpy()), bits(ref["results"][0]))
+    assert np.array_equal(r.per_item[1].cpu().numpy(), ref["results"][1])
+    assert np.array_equal(bits(r.outputs["h"].cpu().numpy()), bits(ref["sums"]["h"]))
+    ct = {"h": torch.linspace(-1, 1, 8)}
+    g = f.grad(x, keys, a, wrt=2, cotangents=ct)
+    J = f.jacfwd(x, keys, a, wrt=2)["h"].cpu().numpy()
+    assert np.isfinite(float(g)) and near(float(g), float(J[0] @ ct["h"].numpy()), 1e-4)

@@ -182,3 +182,27 @@ def test_ph_api_grad_forward_mode_option(cuda):
     assert B.run.last["kernel"] == "ph_grad"
     torch.cuda.synchronize()
     assert near(g1.cpu().numpy(), g2.cpu().numpy())
+
+
+@pytest.mark.parametrize("fn", ["atan", "atan2", "asin", "acos", "tan", "sinh", "cosh", "asinh", "acosh", "atanh",
+                                "exp2", "log2", "cbrt", "erf", "erfc", "erfinv"])
+def test_device_special_math_bitwise_host(cuda, tmlib, orc, fn):
+    """the inverse trigonometric, hyperbolic and erf family: device bitwise host over random bit patterns and
+    in-domain values (NaN inputs and the signed zeros and infinities included)"""
+    rng = np.random.default_rng(11)
+    n = 1 << 18
+    bits = rng.integers(0, 2 ** 32, n, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    dom = {"asin": (-1, 1), "acos": (-1, 1), "atanh": (-1, 1), "erfinv": (-1, 1), "acosh": (1, 50),
+           "tan": (-50, 50), "sinh": (-95, 95), "cosh": (-95, 95), "exp2": (-155, 130), "erf": (-6, 6),
+           "erfc": (-6, 12)}.get(fn, (-100, 100))
+    x = np.concatenate([bits, rng.uniform(*dom, n).astype(np.float32),
+                        np.float32([0.0, -0.0, np.inf, -np.inf, np.nan, 1.0, -1.0])]).astype(np.float32)
+    y = rng.permutation(x).astype(np.float32)
+    host = orc.math(fn, x, y)
+    dx, dy = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    out = torch.empty_like(dx)
+    P = ctypes.c_void_p
+    tmlib.check(tmlib.lib().tm_math_eval(P(torch.cuda.current_stream().cuda_stream), orc.MATH_FN[fn],
+                                         P(dx.data_ptr()), P(dy.data_ptr()), P(out.data_ptr()), len(x)))
+    dev = out.cpu().numpy()
+    assert np.array_equal(dev.view(np.uint32), host.view(np.uint32))
