@@ -197,6 +197,69 @@ def where(c, a, b):
     return T._cur().emit("select", [c, a, b], [a.dtype])[0]
 
 
+def _branch_select(pick, results):
+    """the elementwise selection of branch results of one structure: pick(j) -> bool Var, branch j taken"""
+    flat = [T._flatten(r) for r in results]
+    leaves0, rebuild = flat[0]
+    for lv, _ in flat[1:]:
+        if len(lv) != len(leaves0):
+            raise T.TraceError("tallymap_b200.lang.cond: the branches return different structures")
+    out = []
+    for k in range(len(leaves0)):
+        r = flat[0][0][k]
+        for j in range(1, len(flat)):
+            r = where(pick(j), flat[j][0][k], r)
+        out.append(r)
+    return rebuild(out)
+
+
+def _branches(funs, operands):
+    """trace each branch on the same operands; a branch may not touch the tally (lax.cond of effect-free
+    branches: under vmap both run and a select keeps one, as jax does)"""
+    tr = T._cur()
+    n0 = len(tr.eqns)
+    res = [f(*operands) for f in funs]
+    if any(e.prim in ("emit", "append", "spawn") for e in tr.eqns[n0:]) or \
+            any(isinstance(x, T.TallyToken) for r in res for x in T._flatten(r)[0]):
+        raise T.UnsupportedError("tallymap_b200.lang.cond: a branch that writes the tally is not lowered (select "
+                                 "the value and index, and write once outside the branches)")
+    return res
+
+
+def cond(pred, true_fun, false_fun, *operands):
+    """lax.cond of effect-free branches: both traced, the results selected elementwise by pred"""
+    pred = T._lit(pred)
+    if pred.dtype != T.BOOL:
+        raise T.TraceError("tallymap_b200.lang.cond: the predicate must be bool")
+    f, t = _branches((false_fun, true_fun), operands)
+    return _branch_select(lambda j: pred, (f, t))
+
+
+def switch(index, branches, *operands):
+    """lax.switch of effect-free branches: the index clamped into range, each branch traced, a chain of selects"""
+    index = T._lit(index)
+    if index.dtype != T.I32:
+        raise T.TraceError("tallymap_b200.lang.switch: the index must be int32")
+    n = len(branches)
+    idx = clip(index, 0, n - 1) if isinstance(index, T.Var) else T.Lit(max(0, min(n - 1, int(index.value))), T.I32)
+    res = _branches(branches, operands)
+    return _branch_select(lambda j: idx == j if isinstance(idx, T.Var) else T.Lit(idx.value == j, T.BOOL), res)
+
+
+def fori_loop(lower, upper, body_fun, init_val):
+    """lax.fori_loop with Python int bounds: the body applied upper - lower times, unrolled (an inner loop of a
+    static trip count; the item's one top-level loop stays lax.while_loop)"""
+    if not (isinstance(lower, int) and isinstance(upper, int)):
+        raise T.UnsupportedError("tallymap_b200.lang.fori_loop: Python int bounds only (a traced trip count is a "
+                                 "while_loop)")
+    if upper - lower > 4096:
+        raise T.UnsupportedError("tallymap_b200.lang.fori_loop: at most 4096 unrolled iterations")
+    v = init_val
+    for i in range(lower, upper):
+        v = body_fun(i, v)
+    return v
+
+
 def round(x):   # noqa: A001 (jnp.round)
     """jnp.round: to the nearest integer, ties to even"""
     return _f32("round", x)

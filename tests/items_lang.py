@@ -304,3 +304,17 @@ def special(t, x, key, a):
         return k + 1, s + v, t
     k, s, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
     return t, s, tl.isfinite(s).astype(tl.int32)
+
+
+def branchy(t, x, key, a):
+    """a walk whose step is chosen by lax.cond and lax.switch and smoothed by a static fori_loop"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        dx = tl.cond(u < 0.5, lambda v: -a * v, lambda v: a * (1.0 - v), u)
+        w = tl.switch((u * 3.0).astype(tl.int32), [lambda v: v, lambda v: v * v, lambda v: tl.sqrt(v)], u)
+        w = tl.fori_loop(0, 2, lambda i, s: s * 0.5 + w, w)
+        t = t.add("h", tl.clip((x * 8).astype(tl.int32), 0, 7), w * a)
+        return k + 1, x + 0.1 * dx, t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
+    return t, k

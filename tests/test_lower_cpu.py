@@ -543,3 +543,35 @@ def test_special_math_trace_and_compile():
     uu = np.maximum(lo, f01 * np.float32(2.0) + lo)
     want = (np.float32(np.sqrt(2)) * sp.erfinv(uu.astype(np.float64)).astype(np.float32)).astype(np.float32)
     assert np.array_equal(z.astype(np.float32), want)
+
+
+def test_cond_switch_fori():
+    """lax.cond / switch of effect-free branches become selects (both traced, jax's semantics under vmap);
+    fori_loop with static bounds unrolls; a branch that writes the tally raises UnsupportedError"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, x, key, a):
+        y = tl.cond(x > 0.5, lambda v: (v * a, v + 1.0), lambda v: (v - a, v * 2.0), x)
+        s = tl.switch((x * 4).astype(tl.int32), [lambda v: v, lambda v: -v, lambda v: v * v], x)
+        z = tl.fori_loop(0, 3, lambda i, c: c * 0.5 + i, x)
+        return t.add("h", 0, y[0] + y[1] + s + z), y[0], s, z
+    tr = T.trace_item(item, ["f32", "key", "f32"], 2, {"h": ((1,), "f32")})
+    xs = np.float32([0.1, 0.3, 0.6, 0.9])
+    r = Evaluator(tr, 10).run([xs, prng.split(prng.PRNGKey(0), 4)], [np.float32(2.0)])
+    a = np.float32(2.0)
+    assert np.array_equal(r["results"][0], np.where(xs > 0.5, xs * a, xs - a).astype(np.float32))
+    idx = np.clip((xs * 4).astype(np.int32), 0, 2)
+    assert np.array_equal(r["results"][1], np.choose(idx, [xs, -xs, xs * xs]).astype(np.float32))
+    z = xs
+    for i in range(3):
+        z = (z * np.float32(0.5) + np.float32(i)).astype(np.float32)
+    assert np.array_equal(r["results"][2], z)
+
+    def bad(t, x):
+        t = tl.cond(x > 0.5, lambda tt: tt.add("h", 0, 1.0), lambda tt: tt, t)
+        return t
+    with pytest.raises(tm.UnsupportedError):
+        T.trace_item(bad, ["f32"], 1, {"h": ((1,), "f32")})
+    f = tm.vmap(item, outputs={"h": tm.Sum((1,))}, in_axes=(0, 0, None), max_steps=10)
+    L = f.lowered((xs, prng.split(prng.PRNGKey(0), 4), np.float32(2.0)))
+    assert L.grad_program((0,)).kernel > 0

@@ -800,7 +800,7 @@ def test_broadcast_tables(cuda):
     from items_lang import lookup, neighbours
     from oracle.ir_eval import Evaluator
     rng = np.random.default_rng(5)
-    n = 300
+    n = 150
     x, k = rw_inputs(n, seed=31)
     xs = rng.uniform(0.5, 1.5, 100).astype(np.float32)
     pairs = rng.uniform(-1, 1, (100, 2)).astype(np.float32)
@@ -813,7 +813,7 @@ def test_broadcast_tables(cuda):
     assert np.array_equal(bits(r.outputs["h"].cpu().numpy()), bits(ref["sums"]["h"]))
     assert np.array_equal(r.per_item[0].cpu().numpy(), ref["results"][0])
     assert np.array_equal(bits(r.per_item[1].cpu().numpy()), bits(ref["results"][1]))
-    N = 512
+    N = 256
     pos = rng.uniform(0, 8, (N, 2)).astype(np.float32)
     cell = np.clip((pos[:, 1] / 2).astype(int), 0, 3) * 4 + np.clip((pos[:, 0] / 2).astype(int), 0, 3)
     order = np.argsort(cell, kind="stable").astype(np.int32)
@@ -855,3 +855,22 @@ def test_special_math_item(cuda):
     g = f.grad(x, keys, a, wrt=2, cotangents=ct)
     J = f.jacfwd(x, keys, a, wrt=2)["h"].cpu().numpy()
     assert np.isfinite(float(g)) and near(float(g), float(J[0] @ ct["h"].numpy()), 1e-4)
+
+
+def test_cond_switch_item(cuda):
+    """lax.cond / switch / fori_loop inside the loop body: bitwise against the IR evaluator; the gradient by
+    replay against jacfwd"""
+    from items_lang import branchy
+    from oracle.ir_eval import Evaluator
+    n = 200
+    x, k = rw_inputs(n, seed=37)
+    a = np.float32(1.5)
+    f = tm.vmap(branchy, outputs={"h": tm.Sum((8,), fixed_point=True)}, in_axes=(0, 0, None), max_steps=20000)
+    r = f(x, k, a)
+    ref = Evaluator(f.last_lowered.tr, 20000, ("h",)).run([x, k], [a])
+    assert np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
+    assert np.array_equal(bits(r.outputs["h"].cpu().numpy()), bits(ref["sums"]["h"]))
+    ct = {"h": torch.linspace(-1, 1, 8)}
+    g = f.grad(x, k, a, wrt=2, cotangents=ct)
+    J = f.jacfwd(x, k, a, wrt=2)["h"].cpu().numpy()
+    assert near(float(g), float(J[0] @ ct["h"].numpy()), 1e-4)
