@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the tallymap B200 backend on BASELINE config 2: the 1-D random walk, N = 4,194,304 items per GPU.
+"""Benchmark of the tallymap B200 backend on benchmark configuration 2: the 1-D random walk, N = 4,194,304 items per GPU.
 
 One STEP = the forward outputs plus the reverse-mode gradient (w.r.t. the broadcast `drift`, cotangent ones on the
 hist tally) over the step's items: "Mitems/s fwd & grad".  The step is timed as the ONE value-and-grad launch that
@@ -69,7 +69,7 @@ def q1_inputs(n, start=0, total=None):
 
 
 def od_inputs(n, start=0, total=None):
-    """sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2) (numpy default_rng(3), as the
+    """benchmark configuration 4: sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2) (numpy default_rng(3), as the
     reference's benchmarks make host inputs), item_id = the global item index"""
     total = total or start + n
     rng = np.random.default_rng(3)
@@ -80,7 +80,7 @@ def od_inputs(n, start=0, total=None):
 
 
 def sh_inputs(n, start=0, total=None):
-    """E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
+    """benchmark configuration 5: E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
     from tallymap_b200 import prng
     total = total or start + n
     rng = np.random.default_rng(5)
@@ -107,21 +107,21 @@ def configs(B):
     return {
         "rw": Cfg("rw", B.RW_FWD, B.RW_GRAD, rw_inputs, [1.0], [np.ones(256, np.float32), np.zeros(2, np.float32)],
                   ["hist", "side"], 20000, 2, 0, N_ITEMS,
-                  "1-D random walk (BASELINE config 2): forward + grad w.r.t. drift"),
+                  "1-D random walk (benchmark configuration 2): forward + grad w.r.t. drift"),
         "ph": Cfg("ph", B.PH_FWD, B.PH_GRAD, ph_inputs, [0.1, 10.0], [np.ones((64, 64, 64), np.float32)], ["dep"],
                   100000, 5, 3, N_ITEMS,
-                  "photon slab (BASELINE config 3): forward + grad w.r.t. (mu_a, mu_s)"),
+                  "photon slab (benchmark configuration 3): forward + grad w.r.t. (mu_a, mu_s)"),
         "q1": Cfg("q1", B.Q1_FWD, B.Q1_GRAD, q1_inputs, [2.0], [np.ones(16, np.float32)], ["hist"], 100, 2, 0, 10000,
-                  "quickstart walker (BASELINE config 1): forward + grad w.r.t. theta"),
+                  "quickstart walker (benchmark configuration 1): forward + grad w.r.t. theta"),
         "od": Cfg("od", B.OD_FWD, B.OD_GRAD, od_inputs, [8.0 / 3.0], ["ones(N,3)", np.float32(1.0)],
                   ["final", "mean_z"], 50000, 0, 0, 1048576,
-                  "Lorenz RK45 ensemble (BASELINE config 4): forward + replay grad w.r.t. beta"),
+                  "Lorenz RK45 ensemble (benchmark configuration 4): forward + replay grad w.r.t. beta"),
         # the separate gradient is the tree adjoint: the recording forward, the generation lists, one adjoint launch
         # per generation and one over the roots (backend.tree_grad); the step is the one-pass spawn launch (forward
         # mode through spawn) unless --exact-order
         "sh": Cfg("sh", B.SH_FWD, B.SH_GRAD, sh_inputs, [1.0], [np.ones(512, np.float32)], ["dep", "count"], 100000,
                   0, 0, 1048576,
-                  "branching shower (BASELINE config 5): forward + grad w.r.t. the roots' E0 and X0 (items = roots)"),
+                  "branching shower (benchmark configuration 5): forward + grad w.r.t. the roots' E0 and X0 (items = roots)"),
     }
 
 

@@ -222,7 +222,7 @@ def math(fn, x, y=None):
 
 
 def od_inputs(n, seed=3):
-    """BASELINE config 4's synthetic inputs: sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2), f32"""
+    """benchmark configuration 4's synthetic inputs: sigma ~ U(9, 11), rho ~ U(26, 30), y0 ~ N((1, 1, 1), 0.1^2), f32"""
     rng = np.random.default_rng(seed)
     sigma = rng.uniform(9, 11, n).astype(np.float32)
     rho = rng.uniform(26, 30, n).astype(np.float32)
@@ -259,7 +259,7 @@ def od_grad(sigma, rho, y0, item_id, beta=8.0 / 3.0, ct_final=None, ct_mean=1.0,
 
 
 def sh_inputs(n, seed=5):
-    """BASELINE config 5's primaries: E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
+    """benchmark configuration 5's primaries: E0 = exp(U(0, ln 1000)) (numpy default_rng(5)), depth 0, keys split(PRNGKey(5))"""
     import sys
     import os
     sys.path.insert(0, os.path.dirname(HERE))

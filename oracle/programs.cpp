@@ -201,7 +201,7 @@ struct RWGrad : RWBase {
 };
 
 // ================================================================================================= PH: photon slab
-// The item of BASELINE config 3 (its jax-style source is in tallymap_b200/csrc/items_photon.cuh, restated here):
+// The item of benchmark configuration 3 (its jax-style source is in tallymap_b200/csrc/items_photon.cuh, restated here):
 // per step u = uniform(fold_in(key, k), (4,)); s = -log(1 - u0) / mu_t; p += s d; deposit w * mu_a / mu_t at the
 // clipped voxel when p is inside the 64^3 box; w *= albedo; Henyey-Greenstein (g = 0.9) scattering by (cos_t, phi =
 // 2 pi u2); roulette below 1e-3 with survival u3 < 0.1 (w * 10); the loop runs while the photon is inside and alive.
@@ -405,7 +405,7 @@ static void ph_grad_run(i64 n, const u32* keys, float mu_a, float mu_s, const fl
 }
 
 // ================================================================================================= OD: Lorenz RK45
-// The item of BASELINE config 4 (jax-style source in tallymap_b200/csrc/items_ode.cuh, restated here): Dormand-
+// The item of benchmark configuration 4 (jax-style source in tallymap_b200/csrc/items_ode.cuh, restated here): Dormand-
 // Prince 5(4) with FSAL on the Lorenz field, RMS error norm with atol 1e-9 / rtol 1e-6, step factor
 // clip(0.9 err^-0.2, 0.2, 10) (stop_gradient'ed), t in [0, 10], h0 = 1e-3; the final state is emitted at
 // (item_id, slot) and y_z / 2^20 into a scalar.  Reverse mode restates the hand-derived VJP in the same order.
@@ -586,7 +586,7 @@ struct OdGrad : OdBase {
 };
 
 // ================================================================================================= SH: shower
-// The item of BASELINE config 5 (jax-style source in tallymap_b200/csrc/items_shower.cuh, restated here).  The
+// The item of benchmark configuration 5 (jax-style source in tallymap_b200/csrc/items_shower.cuh, restated here).  The
 // reference runs spawned children through a shared ticket ring on its OpenMP team (kernel.py:778-811, 1007-1044);
 // every child is an independent item, so when the ring drops nothing the tallies are the same sums whatever order
 // the children run in.  The oracle therefore runs each root's whole tree depth-first on one thread (a private stack

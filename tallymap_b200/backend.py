@@ -170,7 +170,7 @@ def canonical_records(p, results, counts):
 _U32 = torch.int32   # uint32 key data travels as int32 bits (torch has no full uint32 arithmetic; bits only)
 
 # -------------------------------------------------------------------------------------------------- programs
-# The benchmark items (BASELINE configs 1 and 2), forward and reverse.  Buffer layouts: csrc/items_walks.cuh.
+# The benchmark items (benchmark configurations 1 and 2), forward and reverse.  Buffer layouts: csrc/items_walks.cuh.
 _F32 = torch.float32
 KEY = Operand("key", (2,), _U32)
 
@@ -207,7 +207,7 @@ Q1_VG1 = ItemProgram("q1_vg_onepass", "q1_vg_onepass", pi=Q1_GRAD.pi, bc=Q1_GRAD
 RW_VG1 = ItemProgram("rw_vg_onepass", "rw_vg_onepass", pi=RW_GRAD.pi, bc=RW_GRAD.bc, consts=("max_steps",),
                      tallies=RW_FWD.tallies + RW_GRAD.tallies, ys=RW_FWD.ys, trunc=1)
 
-# BASELINE config 3, the photon slab (csrc/items_photon.cuh)
+# benchmark configuration 3, the photon slab (csrc/items_photon.cuh)
 PH_FWD = ItemProgram("ph_fwd", "ph_fwd", pi=(KEY,), bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32)),
                      consts=("max_steps",), tallies=(TSpec("dep", (64, 64, 64), f64=True),),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
@@ -217,7 +217,7 @@ PH_GRAD = ItemProgram("ph_grad", "ph_grad", pi=(KEY,),
                       tallies=(TSpec("ct_mu", (2,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=28)
 
-# BASELINE config 4, the Lorenz RK45 ensemble (csrc/items_ode.cuh); "bins3": the final tally's 3N bins
+# benchmark configuration 4, the Lorenz RK45 ensemble (csrc/items_ode.cuh); "bins3": the final tally's 3N bins
 OD_PI = (Operand("sigma", (), _F32), Operand("rho", (), _F32), Operand("y0", (3,), _F32),
          Operand("item_id", (), torch.int32))
 OD_FWD = ItemProgram("od_fwd", "od_fwd", pi=OD_PI, bc=(Operand("beta", (), _F32),), consts=("max_steps", "bins3"),
@@ -229,7 +229,7 @@ OD_GRAD = ItemProgram("od_grad", "od_grad", pi=OD_PI,
                       tallies=(TSpec("ct_beta", (1,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=32)
 
-# BASELINE config 5, the branching shower (csrc/items_shower.cuh): a spawning program with a ring of Q slots
+# benchmark configuration 5, the branching shower (csrc/items_shower.cuh): a spawning program with a ring of Q slots
 SH_FWD = ItemProgram("sh_fwd", "sh_fwd", pi=(Operand("E", (), _F32), Operand("depth", (), _F32), KEY),
                      bc=(Operand("X0", (), _F32),), consts=("max_steps", "queue"),
                      tallies=(TSpec("dep", (512,)), TSpec("count", (1,), torch.int32)),

@@ -1,5 +1,5 @@
 """Item functions written against tallymap_b200.lang, the traced counterparts of the hand-lowered items (the
-reference's examples/quickstart.py:19-30 walker and BASELINE config 2's walk), plus an item that exercises the other
+reference's examples/quickstart.py:19-30 walker and benchmark configuration 2's walk), plus an item that exercises the other
 lowered primitives.  Shared by the lowering tests."""
 from tallymap_b200 import lang as tl
 
@@ -85,7 +85,7 @@ def edges(t, a, key, n, s):
 
 
 def shower(t, E, depth, key, X0):
-    """BASELINE config 5's branching shower as a tallymap user writes it: one particle per item; a split particle
+    """benchmark configuration 5's branching shower as a tallymap user writes it: one particle per item; a split particle
     ends, replaced by two children spawned with the same per-item structure (energy, depth, key)"""
     def body(c):
         k, E, depth, alive, t = c

@@ -1,4 +1,4 @@
-"""GPU parity of the Lorenz RK45 ensemble: trip counts (accepted + rejected steps), truncation
+"""GPU parity of the Lorenz RK45 ensemble (benchmark configuration 4): trip counts (accepted + rejected steps), truncation
 flags, stats, the per-item final states (each bin of Sum((N, 3)) is written by one item, so it is exact) and the
 exact beta gradient bitwise against the oracle; the mean-z scalar within the float-tally tolerance."""
 import numpy as np

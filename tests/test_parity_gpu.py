@@ -190,7 +190,7 @@ def test_rw_edge_inputs(cuda, orc):
 
 # ------------------------------------------------------------------------------------------------ full size
 def test_rw_full_size_properties(cuda):
-    """BASELINE config 2 at N = 4,194,304: size-independent checks (the oracle would take minutes here).
+    """benchmark configuration 2 at N = 4,194,304: size-independent checks (the oracle would take minutes here).
     The gradient of the linear tally drift * x is sum(hist) / drift; the run is bitwise repeatable in every integer
     output and in the exact gradient; every item exits or truncates."""
     n = 4194304

@@ -1,4 +1,4 @@
-"""GPU parity of the photon-slab item and of the shared f32 math it uses.
+"""GPU parity of the photon-slab item (benchmark configuration 3) and of the shared f32 math it uses.
 
 The math (log, exp, sin, cos, pow in tallymap_b200/csrc/tm_math.h) is one implementation compiled for host and
 device, so the device must reproduce the host bitwise; then photon trip counts, truncation flags, stats and the

@@ -1,4 +1,4 @@
-"""GPU parity of the branching shower: the warp-aggregated spawn ring against the oracle's
+"""GPU parity of the branching shower (benchmark configuration 5): the warp-aggregated spawn ring against the oracle's
 depth-first traversal.  With a ring large enough to drop nothing: particle count, spawned children, per-root trip
 counts and truncation flags, and every stat bitwise; the depth deposit within the float-tally tolerance.  With a
 tiny ring: children are dropped and counted, every popped child still runs exactly once, and no wait times out."""
