@@ -1,4 +1,4 @@
-// Item program of the ODE-ensemble configuration: Lorenz systems integrated by adaptive
+// Item program of the ODE-ensemble configuration (benchmark configuration 4): Lorenz systems integrated by adaptive
 // Dormand-Prince 5(4) (FSAL), forward and replay adjoint w.r.t. beta.  The item, as a tallymap user writes it (the
 // tableau and tolerances are Python floats, so each coefficient is a double fraction rounded once to f32):
 //

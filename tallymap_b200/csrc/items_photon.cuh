@@ -1,4 +1,4 @@
-// Item program of the photon-slab configuration, lowered for the runtime: forward and replay
+// Item program of the photon-slab configuration (benchmark configuration 3), lowered for the runtime: forward and replay
 // adjoint w.r.t. (mu_a, mu_s).  The item, as a tallymap user writes it (g, the box and the roulette constants are
 // Python floats, so 1 - g*g etc. are formed in double and rounded once to f32):
 //

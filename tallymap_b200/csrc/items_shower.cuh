@@ -1,4 +1,4 @@
-// Item program of the branching-shower configuration, lowered for the spawn runtime
+// Item program of the branching-shower configuration (benchmark configuration 5), lowered for the spawn runtime
 // (tm_spawn.cuh).  The item, as a tallymap user writes it (one particle; children are spawned with the same inputs):
 //
 //   def particle(t, E, depth, key, X0):                    # per item: E, depth, key; broadcast: X0
