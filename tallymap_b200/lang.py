@@ -28,7 +28,17 @@ float32, int32, uint32, bool_ = "float32", "int32", "uint32", "bool"
 while_loop = T.while_loop
 
 
+pi = 3.141592653589793         # jnp.pi: a Python float, rounded to float32 where it meets a traced value
+e = 2.718281828459045
+
+
+def _vmap1(f, x):
+    return T.Vec(f(v) for v in x) if isinstance(x, T.Vec) else None
+
+
 def _un(prim, x, out=None):
+    if isinstance(x, T.Vec):
+        return _vmap1(lambda v: _un(prim, v, out), x)
     x = T._lit(x)
     if isinstance(x, T.Lit):
         raise T.TraceError(f"tallymap_b200.lang.{prim} of a literal")
@@ -36,6 +46,8 @@ def _un(prim, x, out=None):
 
 
 def _f32(prim, x):
+    if isinstance(x, T.Vec):
+        return _vmap1(lambda v: _f32(prim, v), x)
     x = T._lit(x)
     if x.dtype != T.F32:
         raise T.TraceError(f"tallymap_b200.lang.{prim} takes float32")
@@ -77,6 +89,8 @@ def arctan(x):
 
 def arctan2(y, x):
     """jnp.arctan2(y, x) (lax.atan2): the angle of (x, y) in (-pi, pi], C's signed-zero and infinite cases"""
+    if isinstance(x, T.Vec) or isinstance(y, T.Vec):
+        return T._vec_map2(arctan2, y, x)
     y0 = y if isinstance(y, T.Var) else None
     x0 = x if isinstance(x, T.Var) else None
     y, x = T._lit(y, x0), T._lit(x, y0)
@@ -168,6 +182,8 @@ def abs(x):   # noqa: A001 (jnp.abs)
 
 
 def power(x, y):
+    if isinstance(x, T.Vec) or isinstance(y, T.Vec):
+        return T._vec_map2(power, x, y)
     x0 = x if isinstance(x, T.Var) else None
     y0 = y if isinstance(y, T.Var) else None
     x, y = T._lit(x, y0), T._lit(y, x0)
@@ -186,6 +202,12 @@ def minimum(a, b):
 
 
 def where(c, a, b):
+    if isinstance(c, T.Vec) or isinstance(a, T.Vec) or isinstance(b, T.Vec):
+        n = next(len(v) for v in (c, a, b) if isinstance(v, T.Vec))
+        at = lambda v, i: tuple.__getitem__(v, i) if isinstance(v, T.Vec) else v
+        if any(isinstance(v, T.Vec) and len(v) != n for v in (c, a, b)):
+            raise T.TraceError("tallymap_b200.lang.where: vectors of different lengths")
+        return T.Vec(where(at(c, i), at(a, i), at(b, i)) for i in range(n))
     c = T._lit(c)
     if c.dtype != T.BOOL:
         raise T.TraceError("tallymap_b200.lang.where: the condition must be bool")
@@ -260,6 +282,30 @@ def fori_loop(lower, upper, body_fun, init_val):
     return v
 
 
+def array(xs, dtype=None):
+    """jnp.array / jnp.stack of scalars (traced values or Python numbers) -> a vector with elementwise semantics"""
+    xs = [float(x) if dtype == float32 and isinstance(x, (int, float)) else x for x in xs]
+    v = T.Vec(xs)
+    return v.astype(dtype) if dtype in (float32, int32) and any(isinstance(x, T.Var) for x in xs) else v
+
+
+stack = array
+
+
+def zeros(n, dtype=float32):
+    """jnp.zeros((n,)): a vector of literal zeros"""
+    return T.Vec([0.0 if dtype == float32 else 0] * int(n if isinstance(n, int) else n[0]))
+
+
+def ones(n, dtype=float32):
+    return T.Vec([1.0 if dtype == float32 else 1] * int(n if isinstance(n, int) else n[0]))
+
+
+def dot(a, b):
+    """jnp.dot of two vectors: the products summed left to right"""
+    return sum(T.Vec(a) * T.Vec(b))
+
+
 def round(x):   # noqa: A001 (jnp.round)
     """jnp.round: to the nearest integer, ties to even"""
     return _f32("round", x)
@@ -267,6 +313,8 @@ def round(x):   # noqa: A001 (jnp.round)
 
 def stop_gradient(x):
     """lax.stop_gradient: the value itself, with no derivative (no cotangent, no tangent) through it"""
+    if isinstance(x, T.Vec):
+        return _vmap1(stop_gradient, x)
     x = T._lit(x)
     if isinstance(x, T.Lit):
         return x
@@ -275,6 +323,8 @@ def stop_gradient(x):
 
 def rem(a, b):
     """lax.rem of float32: C's fmod (the sign of a)"""
+    if isinstance(a, T.Vec) or isinstance(b, T.Vec):
+        return T._vec_map2(rem, a, b)
     r = T._binary("rem", a, b)
     if r.dtype != T.F32:
         raise T.TraceError("tallymap_b200.lang.rem takes float32 (use % for integers)")
@@ -283,6 +333,8 @@ def rem(a, b):
 
 def mod(a, b):
     """jnp.mod / jnp.remainder of float32: the sign of b (rem, plus b when the signs differ)"""
+    if isinstance(a, T.Vec) or isinstance(b, T.Vec):
+        return T._vec_map2(mod, a, b)
     r = rem(a, b)
     return where((r != 0.0) & ((r < 0.0) != (b < 0.0)), r + b, r)
 
@@ -383,6 +435,8 @@ def clip(x, a_min, a_max):
 
 def sign(x):
     """jnp.sign (lax.sign): -1, +1, the zero itself for +-0 (its sign kept), NaN for NaN"""
+    if isinstance(x, T.Vec):
+        return _vmap1(sign, x)
     x = T._lit(x)
     if x.dtype == T.F32:
         return where(x > 0.0, 1.0, where(x < 0.0, -1.0, x))
@@ -421,14 +475,14 @@ class random:
     def bits(key, shape=()):
         """jax.random.bits(key, shape, uint32): element i = o0 ^ o1 of threefry2x32(key, (0, i))"""
         n = _count(shape)
-        out = tuple(T._cur().emit("bits", [key.a, key.b, T.Lit(i, T.U32)], [T.U32])[0] for i in range(n))
+        out = T.Vec(T._cur().emit("bits", [key.a, key.b, T.Lit(i, T.U32)], [T.U32])[0] for i in range(n))
         return out[0] if shape == () else out
 
     @staticmethod
     def bernoulli(key, p=0.5, shape=()):
         """jax.random.bernoulli: uniform(key, shape) < p"""
         u = random.uniform(key, shape)
-        return tuple(v < p for v in u) if isinstance(u, tuple) else u < p
+        return u < p
 
     @staticmethod
     def normal(key, shape=(), dtype=float32):
@@ -436,13 +490,13 @@ class random:
         if dtype != float32:
             raise T.TraceError("tallymap_b200.lang.random.normal: float32 only")
         u = random.uniform(key, shape, minval=-0.99999994, maxval=1.0)
-        return tuple(1.41421354 * erfinv(v) for v in u) if isinstance(u, tuple) else 1.41421354 * erfinv(u)
+        return 1.41421354 * erfinv(u)
 
     @staticmethod
     def exponential(key, shape=(), dtype=float32):
         """jax.random.exponential: -log1p(-u) for u = uniform(key, shape)"""
         u = random.uniform(key, shape, dtype)
-        return tuple(-log1p(-v) for v in u) if isinstance(u, tuple) else -log1p(-u)
+        return -log1p(-u)
 
     @staticmethod
     def uniform(key, shape=(), dtype=float32, minval=0.0, maxval=1.0):
@@ -463,7 +517,7 @@ class random:
                     lo32, hi32 = np.float32(lo), np.float32(hi)
                     f = maximum(float(lo32), f * float(np.float32(hi32 - lo32)) + float(lo32))
             out.append(f)
-        return out[0] if shape == () else tuple(out)
+        return out[0] if shape == () else T.Vec(out)
 
 
 def _count(shape):

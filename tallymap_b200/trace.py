@@ -99,6 +99,8 @@ def dtype_of(x):
 
 
 def _binary(prim, a, b, out=None):
+    if isinstance(a, Vec) or isinstance(b, Vec):
+        return _vec_map2(lambda x, y: _binary(prim, x, y, out), a, b)
     a0 = a if isinstance(a, Var) else None
     b0 = b if isinstance(b, Var) else None
     a = _lit(a, b0)
@@ -140,6 +142,17 @@ class Var:
 
     def __ge__(self, o):
         return _binary("ge", self, o, BOOL)
+
+    def __pow__(self, o):
+        """x ** n: lax.integer_pow for a Python int n (binary powering), lax.pow otherwise"""
+        if isinstance(o, int) and not isinstance(o, bool):
+            return int_pow(self, o)
+        from . import lang
+        return lang.power(self, o)
+
+    def __rpow__(self, o):
+        from . import lang
+        return lang.power(o, self)
 
     def __add__(self, o):
         return _binary("add", self, o)
@@ -236,10 +249,73 @@ class Key:
         self.a, self.b = a, b
 
 
+def _vec_map2(f, a, b):
+    la = len(a) if isinstance(a, Vec) else None
+    lb = len(b) if isinstance(b, Vec) else None
+    if la is not None and lb is not None and la != lb:
+        raise TraceError(f"tallymap_b200.lang: vectors of {la} and {lb} elements")
+    n = la if la is not None else lb
+    return Vec(f(tuple.__getitem__(a, i) if la is not None else a, tuple.__getitem__(b, i) if lb is not None else b)
+               for i in range(n))
+
+
+def int_pow(x, n):
+    """x ** n for a Python int n (lax.integer_pow): binary powering, then the reciprocal for n < 0"""
+    if n == 0:
+        return x * 0.0 + 1.0
+    m, acc, base = abs(n), None, x
+    while m > 0:
+        if m & 1:
+            acc = base if acc is None else acc * base
+        m >>= 1
+        if m > 0:
+            base = base * base
+    return 1.0 / acc if n < 0 else acc
+
+
 class Vec(tuple):
-    """a per-item or broadcast float32 vector: a tuple of traced scalars that a traced int32 index also reads
-    (jax.numpy's semantics: a negative index counts from the end, then the index is clamped into range), as a chain
-    of selects, so the element read stays differentiable"""
+    """a small float32 / int32 / bool vector of traced scalars with jax.numpy's elementwise semantics (the item's
+    per-item and broadcast vectors, tl.array / tl.stack): arithmetic, comparisons, logical ops and lang's math
+    functions apply per element, a scalar operand broadcasts; t[i] with a traced int32 index reads an element as
+    jax.numpy does (a negative index counts from the end, then the index is clamped into range) through a chain of
+    selects, so the element read stays differentiable.  Unpacking and iteration are a tuple's."""
+    __hash__ = tuple.__hash__
+
+    @property
+    def shape(self):
+        return (len(self),)
+
+    def _op(prim, out=None):
+        return lambda self, o: _binary(prim, self, o, out)
+
+    def _rop(prim, out=None):
+        return lambda self, o: _binary(prim, o, self, out)
+
+    __add__, __radd__ = _op("add"), _rop("add")
+    __sub__, __rsub__ = _op("sub"), _rop("sub")
+    __mul__, __rmul__ = _op("mul"), _rop("mul")
+    __truediv__, __rtruediv__ = _op("div"), _rop("div")
+    __floordiv__, __mod__ = _op("idiv"), _op("irem")
+    __and__, __rand__, __or__, __ror__, __xor__ = _op("and"), _rop("and"), _op("or"), _rop("or"), _op("xor")
+    __lt__, __le__, __gt__, __ge__ = _op("lt", BOOL), _op("le", BOOL), _op("gt", BOOL), _op("ge", BOOL)
+    __eq__, __ne__ = _op("eq", BOOL), _op("ne", BOOL)
+    del _op, _rop
+
+    def __neg__(self):
+        return Vec(-x for x in tuple.__iter__(self))
+
+    def __invert__(self):
+        return Vec(~x for x in tuple.__iter__(self))
+
+    def __pow__(self, n):
+        return Vec(x ** n for x in tuple.__iter__(self))
+
+    def astype(self, dtype):
+        return Vec(x.astype(dtype) if isinstance(x, Var) else x for x in tuple.__iter__(self))
+
+    def sum(self):
+        from . import lang
+        return lang.sum(self)
 
     def __getitem__(self, i):
         if isinstance(i, (int, slice)) and not isinstance(i, bool):
@@ -496,8 +572,8 @@ def _flatten(tree):
 
     def go(x):
         if isinstance(x, tuple):
-            spec.append(("tuple", len(x)))
-            for y in x:
+            spec.append(("vec" if isinstance(x, Vec) else "tuple", len(x)))
+            for y in tuple.__iter__(x):
                 go(y)
         elif isinstance(x, Key):
             spec.append(("key",))
@@ -515,6 +591,8 @@ def _flatten(tree):
             s = next(sp)
             if s[0] == "tuple":
                 return tuple(build() for _ in range(s[1]))
+            if s[0] == "vec":
+                return Vec(build() for _ in range(s[1]))
             if s[0] == "key":
                 return Key(next(it), next(it))
             return next(it)

@@ -318,3 +318,25 @@ def branchy(t, x, key, a):
         return k + 1, x + 0.1 * dx, t
     k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1), body, (0, x, t))
     return t, k
+
+
+def spheres(t, x0, point, key, theta):
+    """a walk-on-spheres estimator for the Poisson problem on the unit square written with jax.numpy-style vectors
+    (the reference's examples/walk_on_spheres.py problem): a source theta0 exp(-theta1 |y - 1/2|^2) sampled in each
+    ball, boundary values theta2 + theta3 cos(2 pi (x + y)); the estimate tallied at the walker's point"""
+    def dist(x):
+        return tl.minimum(tl.minimum(x[0], 1.0 - x[0]), tl.minimum(x[1], 1.0 - x[1]))
+
+    def body(c):
+        x, acc, k = c
+        R = dist(x)
+        u = tl.random.uniform(tl.random.fold_in(key, k), (3,))
+        r, a = R * tl.sqrt(u[0]), 2.0 * tl.pi * u[1]
+        y = x + r * tl.array([tl.cos(a), tl.sin(a)])
+        src = theta[0] * tl.exp(-theta[1] * tl.sum((y - 0.5) ** 2))
+        acc = acc - 0.25 * R * R * tl.log(tl.maximum(u[0], 1e-20)) * src
+        a2 = 2.0 * tl.pi * u[2]
+        return x + R * tl.stack([tl.cos(a2), tl.sin(a2)]), acc, k + 1
+    x, acc, k = tl.while_loop(lambda c: dist(c[0]) > 1e-3, body, (x0, 0.0, 0))
+    est = acc + theta[2] + theta[3] * tl.cos(2.0 * tl.pi * (x[0] + x[1]))
+    return t.add("u", point, est), k

@@ -575,3 +575,41 @@ def test_cond_switch_fori():
     f = tm.vmap(item, outputs={"h": tm.Sum((1,))}, in_axes=(0, 0, None), max_steps=10)
     L = f.lowered((xs, prng.split(prng.PRNGKey(0), 4), np.float32(2.0)))
     assert L.grad_program((0,)).kernel > 0
+
+
+def test_vector_semantics():
+    """small vectors with jax.numpy's elementwise semantics: arithmetic, broadcasting, comparisons, where, math,
+    integer powers by binary powering, reductions; a walk-on-spheres item written with them traces, evaluates to
+    its scalar restatement and compiles with its gradient"""
+    from oracle.ir_eval import Evaluator
+    from items_lang import spheres
+
+    def item(t, p, key, a):
+        v = tl.array([a, 2.0 * a, 3.0])
+        w = (p + v) * 2.0 - v / a
+        z = tl.where(w > 4.0, w ** 2, -w) + tl.sqrt(tl.abs(p))
+        return t.add("h", 0, tl.sum(z) + tl.dot(p, v)), tl.max(z), (w ** -3)[0], tl.sum(tl.sign(p - 0.5))
+    tr = T.trace_item(item, [("f32", 3), "key", "f32"], 2, {"h": ((1,), "f32")})
+    p = np.float32([[0.1, 0.9, 2.0], [1.0, -2.0, 0.5]])
+    a = np.float32(1.5)
+    r = Evaluator(tr, 10).run([p, prng.split(prng.PRNGKey(0), 2)], [a])
+    f32 = np.float32
+    v = np.array([[a, f32(2.0) * a, f32(3.0)]], np.float32)
+    w = ((p + v) * f32(2.0) - v / a).astype(np.float32)
+    z = (np.where(w > 4.0, w * w, -w) + np.sqrt(np.abs(p))).astype(np.float32)
+    assert np.array_equal(r["results"][0], z.max(1))
+    assert np.array_equal(r["results"][1], (f32(1.0) / (w[:, 0] * (w[:, 0] * w[:, 0]))).astype(np.float32))
+    assert np.array_equal(r["results"][2], np.sign(p - f32(0.5)).sum(1).astype(np.float32))
+    with pytest.raises(T.TraceError):
+        T.trace_item(lambda t, p, k, a: (t, tl.sum(p + tl.array([1.0, 2.0]))), [("f32", 3), "key", "f32"], 2, {})
+    n = 32
+    rng = np.random.default_rng(0)
+    x0 = rng.uniform(0.1, 0.9, (n, 2)).astype(np.float32)
+    point = np.arange(n, dtype=np.int32) % 8
+    keys = prng.split(prng.PRNGKey(4), n)
+    th = np.float32([1.0, 3.0, 0.2, 0.1])
+    f = tm.vmap(spheres, outputs={"u": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=4096)
+    L = f.lowered((x0, point, keys, th))
+    assert L.grad_program((0, 1, 2, 3)).kernel > 0
+    out = Evaluator(L.tr, 4096).run([x0, point, keys], list(th))
+    assert (out["results"][0] > 0).all() and np.isfinite(out["sums"]["u"]).all()
