@@ -74,7 +74,7 @@ def _cur():
 
 
 def _lit(x, like=None):
-    if isinstance(x, Var):
+    if isinstance(x, (Var, Lit)):
         return x
     if isinstance(x, bool):
         return Lit(bool(x), BOOL)
@@ -455,8 +455,23 @@ class TallyToken:
         return self
 
     def add(self, name, index, value):
+        """tally[name][index] += value (_tally.py:248-282): index an int32 (a flat index of a 1-D output) or a
+        tuple of them, one per dimension; a vector index (or coordinate) with a scalar or vector value makes one
+        emit per element, in element order, a scalar broadcast; an index outside the output is dropped and
+        counted in stats['dropped_emits']"""
         if name not in self.specs:
             raise TraceError(f"tallymap_b200.lang: no output named {name!r} (outputs: {sorted(self.specs)})")
+        coords = isinstance(index, tuple) and not isinstance(index, Vec)
+        parts = list(index) if coords else [index]
+        vecs = [p for p in parts + [value] if isinstance(p, Vec)]
+        if vecs:
+            n = len(vecs[0])
+            if any(len(v) != n for v in vecs):
+                raise TraceError(f"tallymap_b200.lang: t.add({name!r}, ...) of vectors of different lengths")
+            at = lambda p, j: tuple.__getitem__(p, j) if isinstance(p, Vec) else p
+            for j in range(n):
+                self.add(name, tuple(at(p, j) for p in parts) if coords else at(index, j), at(value, j))
+            return self
         shape, dt = self.specs[name]
         tr = _cur()
         idx = _flat_index(index, shape)

@@ -613,3 +613,31 @@ def test_vector_semantics():
     assert L.grad_program((0, 1, 2, 3)).kernel > 0
     out = Evaluator(L.tr, 4096).run([x0, point, keys], list(th))
     assert (out["results"][0] > 0).all() and np.isfinite(out["sums"]["u"]).all()
+
+
+def test_add_vectors():
+    """t.add with a vector index and a vector or scalar value: one emit per element (the reference's array emit,
+    _tally.py:248-282), out-of-range elements dropped and counted"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, p, key, a):
+        b = (p * 4.0).astype(tl.int32)
+        t = t.add("h", b, p * a)
+        t = t.add("g", (b, tl.array([0, 1, 2])), 1)
+        return t, tl.sum(b)
+    tr = T.trace_item(item, [("f32", 3), "key", "f32"], 2, {"h": ((4,), "f32"), "g": ((4, 3), "i32")})
+    p = np.float32([[0.1, 0.6, 0.9], [1.2, 0.3, 0.3]])
+    r = Evaluator(tr, 10).run([p, prng.split(prng.PRNGKey(0), 2)], [np.float32(2.0)])
+    h = np.zeros(4, np.float32)
+    g = np.zeros((4, 3), np.int64)
+    dropped = 0
+    for row in p:
+        for j, v in enumerate(row):
+            b = int(np.float32(v) * np.float32(4.0))
+            if 0 <= b < 4:
+                h[b] += np.float32(v) * np.float32(2.0)
+                g[b, j] += 1
+            else:
+                dropped += 2
+    assert np.allclose(r["sums"]["h"], h) and np.array_equal(r["sums"]["g"].reshape(4, 3), g)
+    assert r["stats"][4] == dropped == 2
