@@ -165,10 +165,11 @@ class Mapped:
         bc = [a for a, ax in zip(args, self.fam.in_axes) if ax is None]
         return pi, bc
 
-    def __call__(self, *args):
+    def __call__(self, *args, n_active=None):
+        """the forward launch; n_active: only items i < n_active run (_api.py:466-469)"""
         pi, bc = self._split(args)
         p = self.fam.fwd
-        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.queue)
+        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.queue, n_active=n_active)
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
@@ -461,11 +462,14 @@ class MappedFn:
         got = {w: ct[q].reshape(()) if n is None else ct[q:q + n] for w, (q, n) in where.items()}
         return got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx)
 
-    def __call__(self, *args):
+    def __call__(self, *args, n_active=None):
+        """the forward launch; n_active: only items i < n_active run, the others emit nothing, are never truncated
+        and their per-item results are zero (_api.py:466-469)"""
         L = self.lowered(args)
         pi, bc = self._split(args)
         p = L.fwd
-        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.spawn.capacity if self.spawn else None)
+        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.spawn.capacity if self.spawn else None,
+                    n_active=n_active)
         raw = B.run.last["results"]
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
@@ -491,7 +495,7 @@ class MappedFn:
                 outs[nm] = rec if not bool(n_tr > 0) else _poison(rec, n_tr > 0)
         return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
 
-    def grad(self, *args, wrt, cotangents, order=None):
+    def grad(self, *args, wrt, cotangents, order=None, n_active=None):
         """d <cotangents, outputs> / d args[wrt] for float32 operand(s) `wrt`: ONE replay launch of the generated
         adjoint.  A broadcast operand's cotangent is summed over the items (exactly); a per-item operand's is per
         item (shape (N,) or (N, n)).  -> one cotangent for one index, a tuple in `wrt`'s order for a tuple (for
@@ -512,7 +516,7 @@ class MappedFn:
             c = cotangents.get(name)
             cts.append(torch.zeros(shape, dtype=torch.float32) if c is None else c)
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order,
-                    rev_checkpoints=self.opts["rev_checkpoints"])
+                    rev_checkpoints=self.opts["rev_checkpoints"], n_active=n_active)
         ct = out[0].reshape(-1)
         ys = out[2:]
         bad = ys[prog.trunc].bool().any()
@@ -523,7 +527,7 @@ class MappedFn:
         got.update({w: nan(ys[q]) for q, w in enumerate(pidx)})
         return got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx)
 
-    def jvp(self, *args, wrt, tangents):
+    def jvp(self, *args, wrt, tangents, n_active=None):
         """forward mode (tallymap's jvp of a mapped call, _api.py:305-345): ONE launch of the generated tangent program.
         wrt: float32 broadcast argument index or tuple of indices, W scalars in all (a broadcast vector counts its n
         elements, in order); tangents: W values (one tangent lane) or an
@@ -545,7 +549,7 @@ class MappedFn:
         prog = L_.jvp_program(bpos, L)
         pi, bc = self._split(args)
         out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,),
-                    queue=self.spawn.capacity if self.spawn else None)
+                    queue=self.spawn.capacity if self.spawn else None, n_active=n_active)
         nf = len(L_.fwd.tallies)
         nt = len(prog.tallies)
         tallies = {t.name: v for t, v in zip(prog.tallies[:nf], out[:nf])}

@@ -377,14 +377,16 @@ def _replay_plan(p, max_steps, rev_checkpoints, device):
 
 
 def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_checkpoints=None, order=None,
-        queue=None, record=None, **_):
+        queue=None, record=None, n_active=None, **_):
     """Launch program `p` over the items of `pi` (per-item operands, leading axis N) with broadcast operands `bc`
     and hoisted int32 constants `consts` (max_steps).  -> [sum tallies] + [stats int32[5]] + [per-item results]
     as torch tensors on the current CUDA device, and the raw control words as the attribute-free last element
     of `run.last` (for tm_check_status).  target must be 'cuda' (no CPU fallback, as the reference's kernel
     backend never falls back: _primitive.py:189-194).  out: optional preallocated result buffers (as returned by
     alloc_results), reused without reallocation.  order: optional int32[N] permutation, the order in which the
-    kernel's threads claim items (e.g. longest first, from a primal call's trip counts); it changes no result."""
+    kernel's threads claim items (e.g. longest first, from a primal call's trip counts); it changes no result.
+    n_active: optional item count <= N (the reference's n_active, _api.py:466-469): only items i < n_active run; the
+    others emit nothing, are never truncated and their per-item results are zero (the launch zeroes them)."""
     if target != "cuda":
         raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
     if not torch.cuda.is_available():
@@ -416,6 +418,13 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         known.update(rev_checkpoints=C, replay_threads=threads)
     consts = tuple(known[c] for c in p.consts)
     args.append(_consts(consts or (0,), dev))
+    n_items = N
+    if n_active is not None:
+        n_items = int(n_active)
+        if not 0 <= n_items <= N:
+            raise ValueError(f"{p.name}: n_active must be in [0, {N}], got {n_active}")
+        if order is not None:
+            raise ValueError(f"{p.name}: a claim order and n_active together are not supported")
     if order is not None:
         order = _dev(order, dev, torch.int32)
         if tuple(order.shape) != (N,):
@@ -434,7 +443,9 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         raise _lib.TallymapError(f"{p.name}: layout has {len(ptrs)} buffers, kernel {kernel} takes {nbuf}")
     st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
     flags = (4 if p.spawns else 0) | 8
-    _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], n_zero, N, flags=flags)
+    # (with n_active < N the per-item results, which follow the zeroed buffers, are zeroed too)
+    nz = n_zero + (len(p.ys) if n_items < N else 0)
+    _lib.launch(kid, st, ptrs, len(args), [nb for _, nb, _, _ in layout], nz, n_items, flags=flags)
     names = [n for n, _, _, _ in layout]
     tallies = [res[names.index(t.name)] for t in p.tallies]
     ys = res[n_zero:n_zero + len(p.ys)]

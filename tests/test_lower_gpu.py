@@ -897,3 +897,24 @@ def test_vector_item_spheres(cuda):
     g = f.grad(x0, point, keys, th, wrt=3, cotangents=ct)
     J = f.jacfwd(x0, point, keys, th, wrt=3)["u"].cpu().numpy()
     assert g.shape == (4,) and near(g.cpu().numpy(), J @ ct["u"].numpy(), 1e-4)
+
+
+def test_n_active(cuda):
+    """n_active (_api.py:466-469): only items i < n_active run -- the outputs and the gradient equal those of the
+    prefix bitwise (fixed-point sums), the other items' per-item results are zero and never truncated"""
+    n, m = 3000, 1234
+    x, k = rw_inputs(n, seed=47)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,), fixed_point=True), "side": tm.Sum((2,), fixed_point=True)},
+                in_axes=(0, 0, None), max_steps=20000)
+    d = np.float32(1.0)
+    r = f(x, k, d, n_active=m)
+    rp = f(x[:m], k[:m], d)
+    for nm in ("hist", "side"):
+        assert np.array_equal(bits(r.outputs[nm].cpu().numpy()), bits(rp.outputs[nm].cpu().numpy()))
+    kk = r.per_item.cpu().numpy()
+    assert np.array_equal(kk[:m], rp.per_item.cpu().numpy()) and not kk[m:].any()
+    assert not r.truncated[m:].cpu().numpy().any()
+    ct = {"hist": torch.linspace(0, 1, 256), "side": torch.ones(2)}
+    g = f.grad(x, k, d, wrt=2, cotangents=ct, n_active=m)
+    gp = f.grad(x[:m], k[:m], d, wrt=2, cotangents=ct)
+    assert np.array_equal(bits(g.cpu().numpy()), bits(gp.cpu().numpy()))
