@@ -642,12 +642,3 @@ def test_add_vectors():
     assert np.allclose(r["sums"]["h"], h) and np.array_equal(r["sums"]["g"].reshape(4, 3), g)
     assert r["stats"][4] == dropped == 2
 
-
-def test_n_active_validated():
-    """n_active outside [0, N], or with a claim order, raises before any launch"""
-    import torch
-    from tallymap_b200 import backend as B
-    if torch.cuda.is_available():
-        pytest.skip("checked on the CPU")
-    with pytest.raises(RuntimeError):                # no device here: the check order is device first
-        B.run(B.RW_FWD, list(_args_walk()[:2]), [np.float32(1.0)], consts=(10,), n_active=5)
