@@ -301,6 +301,108 @@ def ones(n, dtype=float32):
     return T.Vec([1.0 if dtype == float32 else 1] * int(n if isinstance(n, int) else n[0]))
 
 
+def prod(xs):
+    """jnp.prod of a vector: the products left to right"""
+    xs = tuple(xs)
+    out = xs[0]
+    for x in xs[1:]:
+        out = out * x
+    return out
+
+
+def mean(xs):
+    """jnp.mean of a float32 vector: the left-to-right sum divided by the length"""
+    return sum(xs) / float(len(xs))
+
+
+def _arg(xs, better):
+    """the first index of the extreme element (jnp.argmax / argmin; a NaN wins, as jax's)"""
+    xs = tuple(xs)
+    best, idx = xs[0], 0
+    for j, x in enumerate(xs[1:], 1):
+        take = better(x, best)
+        if isinstance(x, T.Var) and x.dtype == T.F32:
+            take = take | ((x != x) & (best == best))
+        best, idx = where(take, x, best), where(take, j, idx)
+    return idx
+
+
+def argmax(xs):
+    return _arg(xs, lambda x, b: x > b)
+
+
+def argmin(xs):
+    return _arg(xs, lambda x, b: x < b)
+
+
+def _cum(xs, f):
+    out, acc = [], None
+    for x in tuple(xs):
+        acc = x if acc is None else f(acc, x)
+        out.append(acc)
+    return T.Vec(out)
+
+
+def cumprod(xs):
+    """jnp.cumprod of a vector: the running products, left to right"""
+    return _cum(xs, lambda a, b: a * b)
+
+
+def cummax(xs):
+    """lax.cummax of a vector: the running maxima"""
+    return _cum(xs, maximum)
+
+
+def cummin(xs):
+    return _cum(xs, minimum)
+
+
+def isnan(x):
+    """jnp.isnan: x != x"""
+    return x != x
+
+
+def isinf(x):
+    """jnp.isinf: |x| == inf"""
+    return abs(x) == float("inf")
+
+
+def nan_to_num(x, nan=0.0, posinf=3.4028234663852886e38, neginf=-3.4028234663852886e38):
+    """jnp.nan_to_num of float32: NaN -> nan, +inf -> posinf (the largest float32 by default), -inf -> neginf"""
+    return where(x != x, nan, where(x == float("inf"), posinf, where(x == -float("inf"), neginf, x)))
+
+
+def logaddexp(a, b):
+    """jnp.logaddexp as jax forms it: a + b where a - b is NaN (equal infinities, or a NaN), else
+    max(a, b) + log1p(exp(-|a - b|))"""
+    amax = maximum(a, b)
+    delta = a - b
+    return where(delta != delta, a + b, amax + log1p(exp(-abs(delta))))
+
+
+def hypot(a, b):
+    """jnp.hypot as jax forms it: x = max(|a|, |b|), y = min(...), x sqrt(1 + (y / x)^2) (x itself where it is 0),
+    +inf where either is +-inf"""
+    a, b = abs(a), abs(b)
+    inf = (a == float("inf")) | (b == float("inf"))
+    x, y = maximum(a, b), minimum(a, b)
+    r = where(x == 0.0, x, x * sqrt(1.0 + square(y / where(x == 0.0, 1.0, x))))
+    return where(inf, float("inf"), r)
+
+
+def norm(xs):
+    """jnp.linalg.norm of a vector (the 2-norm): sqrt of the left-to-right sum of squares"""
+    return sqrt(sum(T.Vec(xs) * T.Vec(xs)))
+
+
+def deg2rad(x):
+    return x * (pi / 180.0)
+
+
+def rad2deg(x):
+    return x * (180.0 / pi)
+
+
 def dot(a, b):
     """jnp.dot of two vectors: the products summed left to right"""
     return sum(T.Vec(a) * T.Vec(b))

@@ -642,3 +642,35 @@ def test_add_vectors():
     assert np.allclose(r["sums"]["h"], h) and np.array_equal(r["sums"]["g"].reshape(4, 3), g)
     assert r["stats"][4] == dropped == 2
 
+
+
+def test_numpy_compositions():
+    """jax.numpy functions formed from the lowered primitives, against numpy in float32 on ordinary and awkward
+    values: prod, mean, argmax / argmin (NaN wins, first index), cumprod / cummax / cummin, isnan / isinf,
+    nan_to_num, logaddexp, hypot, norm"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, p, key):
+        v = tl.array(p)
+        return (t, tl.prod(v), tl.mean(v), tl.argmax(v), tl.argmin(v), tl.cumprod(v)[2], tl.cummax(v)[1],
+                tl.cummin(v)[2], tl.isnan(v[0]).astype(tl.int32), tl.isinf(v[1]).astype(tl.int32),
+                tl.nan_to_num(v[1]), tl.logaddexp(v[0], v[1]), tl.hypot(v[1], v[2]), tl.norm(v))
+    tr = T.trace_item(item, [("f32", 3), "key"], 2, {})
+    inf, nan = np.float32(np.inf), np.float32(np.nan)
+    p = np.float32([[0.5, 2.0, -3.0], [1.0, 1.0, 1.0], [nan, 1.0, 2.0], [1.0, inf, 0.0], [-inf, -inf, 4.0],
+                    [0.0, 0.0, 0.0], [1e30, 1e30, 3.0]])
+    r = Evaluator(tr, 1).run([p, prng.split(prng.PRNGKey(0), len(p))], [])["results"]
+    f = np.float32
+    with np.errstate(all="ignore"):
+        want = [p[:, 0] * p[:, 1] * p[:, 2], (p[:, 0] + p[:, 1] + p[:, 2]) / f(3), np.argmax(p, 1), np.argmin(p, 1),
+                np.cumprod(p, 1)[:, 2], np.maximum.accumulate(p, 1)[:, 1], np.minimum.accumulate(p, 1)[:, 2],
+                np.isnan(p[:, 0]), np.isinf(p[:, 1]), np.nan_to_num(p[:, 1]), np.logaddexp(p[:, 0], p[:, 1]),
+                np.hypot(p[:, 1], p[:, 2]), np.sqrt((p * p).sum(1))]
+    for j, (got, w) in enumerate(zip(r, want)):
+        w = np.asarray(w)
+        if w.dtype.kind == "f":
+            w = w.astype(np.float32)
+            ok = np.allclose(got, w, rtol=2e-7, atol=0, equal_nan=True) and np.array_equal(np.isnan(got), np.isnan(w))
+        else:
+            ok = np.array_equal(got, w.astype(np.int64))
+        assert ok, (j, got, w)
