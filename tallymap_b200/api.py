@@ -40,7 +40,8 @@ class Sum:
     fixed_point: bool = False
 
     def __post_init__(self):
-        object.__setattr__(self, "shape", tuple(int(s) for s in self.shape))
+        shape = (self.shape,) if isinstance(self.shape, (int, np.integer)) else self.shape
+        object.__setattr__(self, "shape", tuple(int(s) for s in shape))
         if self.fixed_point and self.dtype != torch.float32:
             raise NotImplementedError("tallymap_b200: fixed_point Sums of float32 only (the exact accumulator)")
 
@@ -677,6 +678,8 @@ def vmap(fn=None, *, outputs, in_axes=0, max_steps=None, spawn=None, backend="au
         return lambda f: vmap(f, outputs=outputs, in_axes=in_axes, max_steps=max_steps, spawn=spawn,
                               backend=backend, **opts)
     o = options(backend, **opts)
+    # a bare shape stands for Sum(shape) (_api.py:509)
+    outputs = {k: (v if isinstance(v, (Sum, Records)) else Sum(v)) for k, v in outputs.items()}
     if callable(fn) and not isinstance(fn, Family):
         return MappedFn(fn, outputs, in_axes, max_steps, spawn, o)
     fam = FAMILIES[fn] if isinstance(fn, str) else fn

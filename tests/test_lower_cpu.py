@@ -674,3 +674,11 @@ def test_numpy_compositions():
         else:
             ok = np.array_equal(got, w.astype(np.int64))
         assert ok, (j, got, w)
+
+
+def test_outputs_shorthand():
+    """a bare shape in outputs is Sum(shape) (_api.py:509); Sum takes an int shape"""
+    from items_lang import walk
+    f = tm.vmap(walk, outputs={"hist": (256,), "side": tm.Sum(2)}, in_axes=(0, 0, None))
+    assert f.outputs == {"hist": ((256,), "f32", False), "side": ((2,), "f32", False)}
+    assert tm.Sum(4).shape == (4,) and tm.Sum(()).shape == ()
