@@ -444,6 +444,14 @@ class MappedFn:
                 bc += [t[i] for i in range(t.shape[0])] if vec else [a]
         return pi, bc
 
+    @staticmethod
+    def _per_item(L, ys):
+        """the flat per-item results regrouped as the item returned them: a vector -> one tensor (N, n); -> the
+        Result's per_item (one value, a tuple, or None)"""
+        groups = L.tr.result_groups or [(j, None) for j in range(len(ys))]
+        per = [ys[f] if n is None else torch.stack(list(ys[f:f + n]), dim=1) for f, n in groups]
+        return per[0] if len(per) == 1 else (tuple(per) or None)
+
     def _bleaves(self, L, idx):
         """-> (the broadcast scalar positions of broadcast arguments idx, in order; argument -> (its first position
         among them, n for a vector or None for a scalar))"""
@@ -494,7 +502,7 @@ class MappedFn:
         if p.records:
             for nm, (rec, _) in recs.items():
                 outs[nm] = rec if not bool(n_tr > 0) else _poison(rec, n_tr > 0)
-        return Result(outs, per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        return Result(outs, self._per_item(L, per[:L.n_results]), trunc, stats)
 
     def grad(self, *args, wrt, cotangents, order=None, n_active=None):
         """d <cotangents, outputs> / d args[wrt] for float32 operand(s) `wrt`: ONE replay launch of the generated
@@ -563,7 +571,7 @@ class MappedFn:
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
         bad = _limits(prog, stats)
-        res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        res = Result(_poison(tallies, bad), self._per_item(L_, per[:L_.n_results]), trunc, stats)
         dts = _poison(dts, bad)
         if not lanes_given:
             dts = {k: v[0] for k, v in dts.items()}
@@ -616,7 +624,7 @@ class MappedFn:
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
         bad = _limits(prog, stats)
-        res = Result(_poison(tallies, bad), per[0] if len(per) == 1 else (tuple(per) or None), trunc, stats)
+        res = Result(_poison(tallies, bad), self._per_item(L, per[:L.n_results]), trunc, stats)
         ct = torch.where(bad, torch.full_like(ct, float("nan")), ct)
         return res, (ct.reshape(()) if isinstance(wrt, int) else ct)
 

@@ -527,6 +527,7 @@ class Traced:
     results: list            # per-item results (Var | Lit)
     specs: dict
     records: dict = dataclasses.field(default_factory=dict)
+    result_groups: list = None   # per returned value: (first flat result, n for a vector or None for a scalar)
 
 
 class _Loop:
@@ -645,7 +646,16 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
     out = out if isinstance(out, tuple) else (out,)
     if not out or not isinstance(out[0], TallyToken):
         raise TallyError("tallymap_b200.lang: an item returns (t, *per_item_results)")
-    results = [_lit(r) for r in out[1:]]
+    results, groups = [], []
+    for r in out[1:]:               # a returned vector: one per-item result per element, regrouped by the API
+        if isinstance(r, tuple):
+            if not r or any(isinstance(x, (tuple, Key, TallyToken)) for x in r):
+                raise TraceError("tallymap_b200.lang: a per-item result is a scalar or a flat vector of scalars")
+            groups.append((len(results), len(r)))
+            results += [_lit(x) for x in r]
+        else:
+            groups.append((len(results), None))
+            results.append(_lit(r))
     pre = tr.eqns[:st["pre_len"]]
     post = tr.eqns[st["pre_len"]:]
     keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
@@ -660,4 +670,4 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
     return Traced(inputs=args, n_per_item=n_per_item, pre=pre, carry_in=[_lit(x) for x in keep(st["init"])],
                   carry=keep(st["carry"]), cond=st["cond"], cond_out=st["cond_out"], body=st["body"],
                   body_out=[_lit(x) for x in keep(st["body_out"])], post_carry=keep(st["post_carry"]), post=post,
-                  results=results, specs=specs, records=records or {})
+                  results=results, specs=specs, records=records or {}, result_groups=groups)

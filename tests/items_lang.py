@@ -340,3 +340,15 @@ def spheres(t, x0, point, key, theta):
     x, acc, k = tl.while_loop(lambda c: dist(c[0]) > 1e-3, body, (x0, 0.0, 0))
     est = acc + theta[2] + theta[3] * tl.cos(2.0 * tl.pi * (x[0] + x[1]))
     return t.add("u", point, est), k
+
+
+def drift2d(t, x0, key, a):
+    """a 2-D walk in the unit square returning its exit point as a vector and its step count"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k), (2,))
+        return k + 1, x + a * (2.0 * u - 1.0), t
+    inside = lambda x: (x[0] > 0.0) & (x[0] < 1.0) & (x[1] > 0.0) & (x[1] < 1.0)
+    k, x, t = tl.while_loop(lambda c: inside(c[1]), body, (0, x0, t))
+    t = t.add("exits", (x[0] > 1.0).astype(tl.int32) + 2 * (x[1] > 1.0).astype(tl.int32), 1.0)
+    return t, x, k

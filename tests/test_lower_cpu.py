@@ -682,3 +682,21 @@ def test_outputs_shorthand():
     f = tm.vmap(walk, outputs={"hist": (256,), "side": tm.Sum(2)}, in_axes=(0, 0, None))
     assert f.outputs == {"hist": ((256,), "f32", False), "side": ((2,), "f32", False)}
     assert tm.Sum(4).shape == (4,) and tm.Sum(()).shape == ()
+
+
+def test_vector_results():
+    """an item returning a vector: one flat per-item result per element, regrouped into an (N, n) array"""
+    import torch
+    from oracle.ir_eval import Evaluator
+    from items_lang import drift2d
+    n = 16
+    x0 = np.random.default_rng(1).uniform(0.3, 0.7, (n, 2)).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(2), n)
+    f = tm.vmap(drift2d, outputs={"exits": tm.Sum((4,))}, in_axes=(0, 0, None), max_steps=10000)
+    L = f.lowered((x0, keys, np.float32(0.1)))
+    assert L.tr.result_groups == [(0, 2), (2, None)] and L.n_results == 3
+    r = Evaluator(L.tr, 10000).run([x0, keys], [np.float32(0.1)])
+    ys = [torch.from_numpy(np.asarray(v)) for v in r["results"]]
+    xy, k = f._per_item(L, ys)
+    assert tuple(xy.shape) == (n, 2) and tuple(k.shape) == (n,)
+    assert ((xy <= 0) | (xy >= 1)).any(dim=1).all()

@@ -918,3 +918,20 @@ def test_n_active(cuda):
     g = f.grad(x, k, d, wrt=2, cotangents=ct, n_active=m)
     gp = f.grad(x[:m], k[:m], d, wrt=2, cotangents=ct)
     assert np.array_equal(bits(g.cpu().numpy()), bits(gp.cpu().numpy()))
+
+
+def test_vector_results(cuda):
+    """an item returning a vector: Result.per_item holds an (N, 2) array bitwise the evaluator's"""
+    from items_lang import drift2d
+    from oracle.ir_eval import Evaluator
+    n = 500
+    x0 = np.random.default_rng(3).uniform(0.3, 0.7, (n, 2)).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(5), n)
+    f = tm.vmap(drift2d, outputs={"exits": tm.Sum((4,))}, in_axes=(0, 0, None), max_steps=10000)
+    r = f(x0, keys, np.float32(0.1))
+    xy, k = r.per_item
+    ref = Evaluator(f.last_lowered.tr, 10000).run([x0, keys], [np.float32(0.1)])
+    assert tuple(xy.shape) == (n, 2)
+    assert np.array_equal(bits(xy[:, 0].cpu().numpy()), bits(ref["results"][0]))
+    assert np.array_equal(bits(xy[:, 1].cpu().numpy()), bits(ref["results"][1]))
+    assert np.array_equal(k.cpu().numpy(), ref["results"][2])
