@@ -601,6 +601,43 @@ class random:
         return -log1p(-u)
 
     @staticmethod
+    def gumbel(key, shape=(), dtype=float32):
+        """jax.random.gumbel: -log(-log(u)) for u = uniform(key, shape, minval=float32 tiny, maxval=1)"""
+        u = random.uniform(key, shape, dtype, minval=1.1754943508222875e-38, maxval=1.0)
+        return -log(-log(u))
+
+    @staticmethod
+    def categorical(key, logits):
+        """jax.random.categorical over a vector of logits: argmax(gumbel(key, (n,)) + logits), an int32 index"""
+        logits = T.Vec(logits)
+        return argmax(random.gumbel(key, (len(logits),)) + logits)
+
+    @staticmethod
+    def randint(key, shape=(), minval=0, maxval=2):
+        """jax.random.randint for int32 Python-int bounds: two 32-bit draws from split(key) combined modulo the
+        span (2^32 mod span folded in through its square root), minval where maxval <= minval"""
+        if not (isinstance(minval, int) and isinstance(maxval, int)):
+            raise T.UnsupportedError("tallymap_b200.lang.random.randint: Python int bounds only")
+        import builtins
+        lo = builtins.max(-2 ** 31, builtins.min(2 ** 31 - 1, minval))
+        hi = builtins.max(-2 ** 31, builtins.min(2 ** 31 - 1, maxval))
+        out_of_range = maxval > 2 ** 31 - 1
+        span = (hi - lo) & 0xFFFFFFFF if hi > lo else 1
+        if out_of_range and hi > lo:
+            span = (span + 1) & 0xFFFFFFFF
+        k1, k2 = random.split(key)
+        hb, lb = random.bits(k1, shape), random.bits(k2, shape)
+        mult = (2 ** 16) % span if span else 0
+        mult = (mult * mult) % span if span else 0
+
+        def one(h, l):
+            off = (h % span) * mult + (l % span)
+            return (off % span).astype(int32) + lo
+        if span == 0:          # (the full 2^32 range: the wrapped span is 0 and jax's remainders are by 0)
+            raise T.UnsupportedError("tallymap_b200.lang.random.randint: a span of 2^32 is not lowered")
+        return T.Vec(one(h, l) for h, l in zip(hb, lb)) if shape != () else one(hb, lb)
+
+    @staticmethod
     def uniform(key, shape=(), dtype=float32, minval=0.0, maxval=1.0):
         """jax.random.uniform: the mantissa fill of random bits in [1, 2) minus 1, then max(lo, f * (hi - lo) + lo)"""
         if dtype != float32:

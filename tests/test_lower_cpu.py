@@ -700,3 +700,33 @@ def test_vector_results():
     xy, k = f._per_item(L, ys)
     assert tuple(xy.shape) == (n, 2) and tuple(k.shape) == (n,)
     assert ((xy <= 0) | (xy >= 1)).any(dim=1).all()
+
+
+def test_randint_gumbel_categorical():
+    """random.randint (in [minval, maxval), equal to its arithmetic restated in numpy on the same bits; minval when
+    maxval <= minval), random.gumbel (-log(-log u)) and random.categorical (the Gumbel-max choice: frequencies near
+    softmax(logits))"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, key):
+        return (t, tl.random.randint(key, (), -3, 10), tl.random.randint(key, (2,), 5, 5)[1],
+                tl.random.categorical(key, tl.array([0.0, 1.0, -1.0, 0.5])), tl.random.gumbel(key))
+    tr = T.trace_item(item, ["key"], 1, {})
+    n = 4000
+    keys = prng.split(prng.PRNGKey(21), n)
+    r = Evaluator(tr, 1).run([keys], [])["results"]
+    ri, same, cat, g = r
+    assert ri.min() == -3 and ri.max() == 9 and (same == 5).all()
+    k1 = np.array([prng.threefry2x32(np.uint32(k[0]), np.uint32(k[1]), np.uint32(0), np.uint32(0)) for k in keys])
+    k2 = np.array([prng.threefry2x32(np.uint32(k[0]), np.uint32(k[1]), np.uint32(0), np.uint32(1)) for k in keys])
+    bits = lambda kk: np.array([np.bitwise_xor(*prng.threefry2x32(np.uint32(a), np.uint32(b), np.uint32(0),
+                                                                  np.uint32(0))) for a, b in kk], np.uint64)
+    span = 13
+    mult = (65536 % span) ** 2 % span
+    want = (((bits(k1) % span) * mult + bits(k2) % span) % (2 ** 32) % span).astype(np.int64) - 3
+    assert np.array_equal(ri, want)
+    p = np.exp([0.0, 1.0, -1.0, 0.5])
+    p /= p.sum()
+    freq = np.bincount(cat, minlength=4) / n
+    assert np.abs(freq - p).max() < 0.03
+    assert abs(float(np.mean(g)) - 0.5772) < 0.06
