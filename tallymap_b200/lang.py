@@ -408,6 +408,33 @@ def dot(a, b):
     return sum(T.Vec(a) * T.Vec(b))
 
 
+def scan(f, init, xs=None, length=None):
+    """lax.scan with a static length (len(xs), or `length`), unrolled: carry, y = f(carry, x) per step; -> (the
+    final carry, the ys stacked: a vector of the per-step scalars, a tuple of vectors for tuple outputs, None for
+    None).  xs: a vector, or a tuple of vectors scanned together"""
+    if xs is None:
+        if not isinstance(length, int):
+            raise T.UnsupportedError("tallymap_b200.lang.scan: a static length (Python int) or xs")
+        n, at = length, (lambda i: None)
+    elif isinstance(xs, tuple) and not isinstance(xs, T.Vec) and xs and isinstance(xs[0], tuple):
+        n = len(xs[0])
+        at = lambda i: tuple(tuple.__getitem__(x, i) for x in xs)
+    else:
+        n = len(xs)
+        at = lambda i: tuple.__getitem__(xs, i)
+    if n > 4096:
+        raise T.UnsupportedError("tallymap_b200.lang.scan: at most 4096 unrolled steps")
+    carry, ys = init, []
+    for i in range(n):
+        carry, y = f(carry, at(i))
+        ys.append(y)
+    if not ys or ys[0] is None:
+        return carry, None
+    if isinstance(ys[0], tuple) and not isinstance(ys[0], T.Vec):
+        return carry, tuple(T.Vec(y[j] for y in ys) for j in range(len(ys[0])))
+    return carry, T.Vec(ys)
+
+
 def round(x):   # noqa: A001 (jnp.round)
     """jnp.round: to the nearest integer, ties to even"""
     return _f32("round", x)

@@ -730,3 +730,23 @@ def test_randint_gumbel_categorical():
     freq = np.bincount(cat, minlength=4) / n
     assert np.abs(freq - p).max() < 0.03
     assert abs(float(np.mean(g)) - 0.5772) < 0.06
+
+
+def test_scan():
+    """lax.scan with a static length, unrolled: the final carry and the stacked outputs"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, p, key):
+        c, ys = tl.scan(lambda c, x: (c * 0.5 + x, c + x), 0.0, p)
+        c2, (a, b) = tl.scan(lambda c, _: (c + 1.0, (c, c * c)), 1.0, length=3)
+        return t, c, ys[2], tl.sum(a) + tl.sum(b) + c2
+    tr = T.trace_item(item, [("f32", 3), "key"], 1, {})
+    p = np.float32([[1.0, 2.0, 4.0], [0.5, -1.0, 3.0]])
+    r = Evaluator(tr, 1).run([p, prng.split(prng.PRNGKey(0), 2)], [])["results"]
+    for row, c, y2 in zip(p, r[0], r[1]):
+        cc, ys = np.float32(0), []
+        for x in row:
+            ys.append(cc + x)
+            cc = cc * np.float32(0.5) + x
+        assert c == cc and y2 == ys[2]
+    assert (r[2] == np.float32(1 + 2 + 3 + 1 + 4 + 9 + 4)).all()
