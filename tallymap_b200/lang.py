@@ -4,8 +4,10 @@ jax.random and lax.while_loop with jax's semantics, the ones the reference's op 
 random_bits / fold_in / split, while, round, rem, stop_gradient), and compositions of them with jax's semantics
 (clip, sign, square, mod, log1p, expm1, tanh, the reductions sum / max / min / all / any, cumsum and searchsorted
 over a per-item vector, random.bernoulli); the inverse trigonometric, hyperbolic, exp2 / log2 / cbrt and erf / erfc /
-erfinv primitives (random.normal over erfinv as jax.random forms it, random.exponential), ceil, log10, logistic and
-isfinite as jax.numpy forms them.
+erfinv primitives (random.normal over erfinv as jax.random forms it, random.exponential, gumbel, categorical,
+randint), ceil, log10, logistic, isfinite and the other jax.numpy compositions below; small vectors with jax.numpy's
+elementwise semantics (trace.Vec: array, stack, dot, reductions, a traced index read as jnp does); broadcast tables
+read by traced indices (trace.Table); cond / switch of effect-free branches and fori_loop / scan of static lengths.
 
     from tallymap_b200 import lang as tl
 
