@@ -286,6 +286,7 @@ def fori_loop(lower, upper, body_fun, init_val):
 
 def array(xs, dtype=None):
     """jnp.array / jnp.stack of scalars (traced values or Python numbers) -> a vector with elementwise semantics"""
+    xs = [x.item() if hasattr(x, "item") and not isinstance(x, (T.Var, T.Lit)) else x for x in xs]   # numpy numbers
     xs = [float(x) if dtype == float32 and isinstance(x, (int, float)) else x for x in xs]
     v = T.Vec(xs)
     return v.astype(dtype) if dtype in (float32, int32) and any(isinstance(x, T.Var) for x in xs) else v

@@ -750,3 +750,24 @@ def test_scan():
             cc = cc * np.float32(0.5) + x
         assert c == cc and y2 == ys[2]
     assert (r[2] == np.float32(1 + 2 + 3 + 1 + 4 + 9 + 4)).all()
+
+
+def test_constant_vector_lookup():
+    """a constant vector (numpy or Python numbers) read by a traced index, as a Gillespie item's state-change table
+    jnp.array([1, -1, 1, -1])[r]: a chain of selects of literals, clamped as jax.numpy clamps"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, x, key):
+        r = (x * 4.0).astype(tl.int32)
+        dx = tl.array(np.array([1, -1, 1, -1], np.int32))[r]
+        w = tl.array([0.5, 1.5, 2.5, 3.5])[r - 1]
+        return t, dx, w
+    tr = T.trace_item(item, ["f32", "key"], 1, {})
+    xs = np.float32([0.0, 0.3, 0.6, 0.9, 2.0, -1.0])
+    r = Evaluator(tr, 1).run([xs, prng.split(prng.PRNGKey(0), len(xs))], [])["results"]
+    idx = (xs * 4).astype(np.int32)
+    tab = np.array([1, -1, 1, -1])
+    assert np.array_equal(r[0], tab[np.clip(np.where(idx < 0, idx + 4, idx), 0, 3)])
+    w = np.float32([0.5, 1.5, 2.5, 3.5])
+    j = idx - 1
+    assert np.array_equal(r[1], w[np.clip(np.where(j < 0, j + 4, j), 0, 3)])
