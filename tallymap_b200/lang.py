@@ -643,6 +643,25 @@ class random:
         return argmax(random.gumbel(key, (len(logits),)) + logits)
 
     @staticmethod
+    def choice(key, a, shape=(), replace=True, p=None):
+        """jax.random.choice with replacement: an index drawn by randint(0, n) (p None) or by inverse-CDF sampling,
+        searchsorted(cumsum(p), cumsum(p)[-1] * (1 - uniform)); the index itself for an int `a`, else a[index]"""
+        if not replace:
+            raise T.UnsupportedError("tallymap_b200.lang.random.choice: replace=False is not lowered")
+        n = a if isinstance(a, int) else len(a)
+        if p is None:
+            ind = random.randint(key, shape, 0, n)
+        else:
+            pc = cumsum(T.Vec(p))
+            u = random.uniform(key, shape)
+            draw = lambda v: searchsorted(pc, pc[-1] * (1.0 - v))
+            ind = T.Vec(draw(v) for v in u) if isinstance(u, T.Vec) else draw(u)
+        if isinstance(a, int):
+            return ind
+        av = T.Vec(a)
+        return T.Vec(av[i] for i in ind) if isinstance(ind, T.Vec) else av[ind]
+
+    @staticmethod
     def randint(key, shape=(), minval=0, maxval=2):
         """jax.random.randint for int32 Python-int bounds: two 32-bit draws from split(key) combined modulo the
         span (2^32 mod span folded in through its square root), minval where maxval <= minval"""

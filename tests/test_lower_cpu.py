@@ -771,3 +771,22 @@ def test_constant_vector_lookup():
     w = np.float32([0.5, 1.5, 2.5, 3.5])
     j = idx - 1
     assert np.array_equal(r[1], w[np.clip(np.where(j < 0, j + 4, j), 0, 3)])
+
+
+def test_random_choice():
+    """random.choice with replacement: with p, the inverse-CDF index searchsorted(cumsum(p), total (1 - u)) (restated
+    in numpy on the same uniforms) and frequencies near p; without p, randint(0, n); values taken from a vector"""
+    from oracle.ir_eval import Evaluator
+    p = [0.1, 0.6, 0.3]
+
+    def item(t, key):
+        return (t, tl.random.choice(key, 3, p=tl.array(p)), tl.random.choice(key, tl.array([2.0, 4.0, 8.0])),
+                tl.random.uniform(key))
+    tr = T.trace_item(item, ["key"], 1, {})
+    n = 3000
+    r = Evaluator(tr, 1).run([prng.split(prng.PRNGKey(9), n)], [])["results"]
+    pc = np.cumsum(np.float32(p), dtype=np.float32)
+    want = np.searchsorted(pc, (pc[-1] * (np.float32(1) - r[2])).astype(np.float32), side="left")
+    assert np.array_equal(r[0], want)
+    assert np.abs(np.bincount(r[0], minlength=3) / n - np.array(p)).max() < 0.03
+    assert set(np.unique(r[1])) <= {2.0, 4.0, 8.0}
