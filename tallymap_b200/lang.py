@@ -631,6 +631,18 @@ class random:
         return -log1p(-u)
 
     @staticmethod
+    def laplace(key, shape=(), dtype=float32):
+        """jax.random.laplace: sign(u) log1p(-|u|) for u = uniform(key, shape, minval=-1 + 2^-24, maxval=1)"""
+        u = random.uniform(key, shape, dtype, minval=-0.99999994, maxval=1.0)
+        return sign(u) * log1p(-abs(u))
+
+    @staticmethod
+    def rademacher(key, shape=(), dtype=int32):
+        """jax.random.rademacher: 2 bernoulli(key, 0.5, shape) - 1, as int32 (+-1)"""
+        b = random.bernoulli(key, 0.5, shape).astype(int32)
+        return 2 * b - 1
+
+    @staticmethod
     def gumbel(key, shape=(), dtype=float32):
         """jax.random.gumbel: -log(-log(u)) for u = uniform(key, shape, minval=float32 tiny, maxval=1)"""
         u = random.uniform(key, shape, dtype, minval=1.1754943508222875e-38, maxval=1.0)

@@ -790,3 +790,16 @@ def test_random_choice():
     assert np.array_equal(r[0], want)
     assert np.abs(np.bincount(r[0], minlength=3) / n - np.array(p)).max() < 0.03
     assert set(np.unique(r[1])) <= {2.0, 4.0, 8.0}
+
+
+def test_laplace_rademacher():
+    """random.laplace (sign(u) log1p(-|u|): symmetric, mean |x| near 1) and random.rademacher (+-1, balanced)"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, key):
+        return t, tl.random.laplace(key), tl.random.rademacher(key, (2,))[1]
+    tr = T.trace_item(item, ["key"], 1, {})
+    n = 4000
+    r = Evaluator(tr, 1).run([prng.split(prng.PRNGKey(10), n)], [])["results"]
+    assert abs(float(np.mean(r[0]))) < 0.1 and abs(float(np.mean(np.abs(r[0]))) - 1.0) < 0.08
+    assert set(np.unique(r[1])) == {-1, 1} and abs(float(np.mean(r[1]))) < 0.06
