@@ -631,6 +631,23 @@ class random:
         return -log1p(-u)
 
     @staticmethod
+    def truncated_normal(key, lower, upper, shape=(), dtype=float32):
+        """jax.random.truncated_normal for Python-number bounds: u uniform on (erf(lower / sqrt2), erf(upper /
+        sqrt2)), sqrt2 erfinv(u), clipped inside (lower, upper) by one float32 step (the bounds' erf in float32,
+        correctly rounded as the shared math's)"""
+        if not (isinstance(lower, (int, float)) and isinstance(upper, (int, float))):
+            raise T.UnsupportedError("tallymap_b200.lang.random.truncated_normal: Python-number bounds only")
+        import math
+        import numpy as np
+        s2 = np.float32(math.sqrt(2.0))
+        lo, hi = np.float32(lower), np.float32(upper)
+        ea = float(np.float32(math.erf(float(np.float32(lo / s2)))))
+        eb = float(np.float32(math.erf(float(np.float32(hi / s2)))))
+        u = random.uniform(key, shape, dtype, minval=ea, maxval=eb)
+        out = float(s2) * erfinv(u)
+        return clip(out, float(np.nextafter(lo, np.float32(np.inf))), float(np.nextafter(hi, np.float32(-np.inf))))
+
+    @staticmethod
     def laplace(key, shape=(), dtype=float32):
         """jax.random.laplace: sign(u) log1p(-|u|) for u = uniform(key, shape, minval=-1 + 2^-24, maxval=1)"""
         u = random.uniform(key, shape, dtype, minval=-0.99999994, maxval=1.0)

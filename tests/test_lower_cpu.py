@@ -803,3 +803,14 @@ def test_laplace_rademacher():
     r = Evaluator(tr, 1).run([prng.split(prng.PRNGKey(10), n)], [])["results"]
     assert abs(float(np.mean(r[0]))) < 0.1 and abs(float(np.mean(np.abs(r[0]))) - 1.0) < 0.08
     assert set(np.unique(r[1])) == {-1, 1} and abs(float(np.mean(r[1]))) < 0.06
+
+
+def test_truncated_normal():
+    """random.truncated_normal: inside (lower, upper), the standard normal's mean on [-1, 2] (about 0.2297)"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, key):
+        return t, tl.random.truncated_normal(key, -1.0, 2.0)
+    tr = T.trace_item(item, ["key"], 1, {})
+    r = Evaluator(tr, 1).run([prng.split(prng.PRNGKey(11), 4000)], [])["results"][0]
+    assert r.min() > -1.0 and r.max() < 2.0 and abs(float(r.mean()) - 0.2297) < 0.05
