@@ -552,12 +552,38 @@ def searchsorted(a, v, side="left"):
     ("right"), as int32"""
     if side not in ("left", "right"):
         raise T.TraceError("tallymap_b200.lang.searchsorted: side 'left' or 'right'")
+    if isinstance(a, T.Table):
+        # a sorted 1-D table: binary search, bit_length(n) steps unrolled, each a gather and two selects
+        if len(a.shape) != 1:
+            raise T.TraceError("tallymap_b200.lang.searchsorted: a 1-D table")
+        n = a.shape[0]
+        lo, hi = 0, n
+        for _ in range(n.bit_length()):
+            act = T.Lit(True, T.BOOL) if isinstance(lo, int) and isinstance(hi, int) else (lo < hi)
+            mid = (lo + hi) // 2
+            c = (a[mid] < v) if side == "left" else (a[mid] <= v)
+            lo, hi = where(act & c, mid + 1, lo), where(act & ~c, mid, hi)
+        return lo
     cnt = None
     for x in a:
         c = (x < v) if side == "left" else (x <= v)
         c = c.astype(int32)
         cnt = c if cnt is None else cnt + c
     return cnt
+
+
+def interp(x, xp, fp, left=None, right=None):
+    """jnp.interp as jax forms it: i = clip(searchsorted(xp, x, 'right'), 1, n - 1), fp[i-1] + (x - xp[i-1]) /
+    (xp[i] - xp[i-1]) (fp[i] - fp[i-1]) (fp[i-1] where the step is below 2^-46), fp[0] / fp[-1] (or left / right)
+    outside [xp[0], xp[-1]]; xp and fp vectors or 1-D tables"""
+    n = len(xp)
+    i = clip(searchsorted(xp, x, side="right"), 1, n - 1)
+    xi, xm, fi, fm = xp[i], xp[i - 1], fp[i], fp[i - 1]
+    df, dx, delta = fi - fm, xi - xm, x - xm
+    dx0 = abs(dx) <= 1.4210854715202004e-14
+    f = where(dx0, fm, fm + (delta / where(dx0, 1.0, dx)) * df)
+    f = where(x < xp[0], fp[0] if left is None else left, f)
+    return where(x > xp[-1], fp[-1] if right is None else right, f)
 
 
 def clip(x, a_min, a_max):

@@ -814,3 +814,27 @@ def test_truncated_normal():
     tr = T.trace_item(item, ["key"], 1, {})
     r = Evaluator(tr, 1).run([prng.split(prng.PRNGKey(11), 4000)], [])["results"][0]
     assert r.min() > -1.0 and r.max() < 2.0 and abs(float(r.mean()) - 0.2297) < 0.05
+
+
+def test_interp_and_table_search():
+    """searchsorted over a sorted table (an unrolled binary search) equals numpy's; interp over a vector and over
+    tables equals its float32 formula and is close to numpy's float64 interp"""
+    from oracle.ir_eval import Evaluator
+    xp = np.float32([0.0, 0.1, 0.1, 0.4, 1.0, 2.5, 3.0])
+    fp = np.float32([1.0, 2.0, 3.0, -1.0, 0.5, 4.0, 4.5])
+
+    def item(t, x, key, txp, tfp):
+        return (t, tl.searchsorted(txp, x), tl.searchsorted(txp, x, side="right"), tl.interp(x, txp, tfp),
+                tl.interp(x, tl.array(list(xp)), tl.array(list(fp)), left=-9.0))
+    tr = T.trace_item(item, ["f32", "key", ("table", "f32", (7,)), ("table", "f32", (7,))], 2, {})
+    x = np.float32([-1.0, 0.0, 0.05, 0.1, 0.2, 0.4, 2.0, 2.9999, 3.0, 5.0])
+    r = Evaluator(tr, 1).run([x, prng.split(prng.PRNGKey(0), len(x))], [xp, fp])["results"]
+    assert np.array_equal(r[0], np.searchsorted(xp, x, "left"))
+    assert np.array_equal(r[1], np.searchsorted(xp, x, "right"))
+    i = np.clip(np.searchsorted(xp, x, "right"), 1, 6)
+    dx = xp[i] - xp[i - 1]
+    want = np.where(dx == 0, fp[i - 1], fp[i - 1] + ((x - xp[i - 1]) / np.where(dx == 0, 1, dx)) * (fp[i] - fp[i - 1]))
+    want = np.where(x < xp[0], fp[0], np.where(x > xp[-1], fp[-1], want)).astype(np.float32)
+    assert np.array_equal(r[2], want)
+    assert np.allclose(r[2], np.interp(x, xp, fp), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(r[3], np.where(x < 0, np.float32(-9), want))
