@@ -572,6 +572,32 @@ def searchsorted(a, v, side="left"):
     return cnt
 
 
+def _sorted_pairs(xs):
+    """odd-even transposition sort of a vector with its indices: n passes of adjacent compare-exchanges, a swap
+    when the right element is smaller or the left is NaN (NaNs last, as jnp.sort); equal elements never swap, so
+    the order is stable"""
+    v = list(tuple(xs))
+    idx = list(range(len(v)))
+    n = len(v)
+    for p in range(n):
+        for j in range(p % 2, n - 1, 2):
+            a, b = v[j], v[j + 1]
+            swap = (b < a) | ((a != a) & (b == b)) if isinstance(a, T.Var) and a.dtype == T.F32 else (b < a)
+            v[j], v[j + 1] = where(swap, b, a), where(swap, a, b)
+            idx[j], idx[j + 1] = where(swap, idx[j + 1], idx[j]), where(swap, idx[j], idx[j + 1])
+    return T.Vec(v), T.Vec(idx)
+
+
+def sort(xs):
+    """jnp.sort of a vector: ascending, NaNs last, stable"""
+    return _sorted_pairs(xs)[0]
+
+
+def argsort(xs):
+    """jnp.argsort of a vector: the stable ascending order's indices (int32)"""
+    return _sorted_pairs(xs)[1]
+
+
 def interp(x, xp, fp, left=None, right=None):
     """jnp.interp as jax forms it: i = clip(searchsorted(xp, x, 'right'), 1, n - 1), fp[i-1] + (x - xp[i-1]) /
     (xp[i] - xp[i-1]) (fp[i] - fp[i-1]) (fp[i-1] where the step is below 2^-46), fp[0] / fp[-1] (or left / right)

@@ -838,3 +838,25 @@ def test_interp_and_table_search():
     assert np.array_equal(r[2], want)
     assert np.allclose(r[2], np.interp(x, xp, fp), rtol=1e-5, atol=1e-6)
     assert np.array_equal(r[3], np.where(x < 0, np.float32(-9), want))
+
+
+def test_sort_argsort():
+    """sort / argsort of a vector (a sorting network of compare-exchanges): ascending, NaNs last, stable (numpy's
+    stable sort on the same values, the signed zeros kept in their input order)"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, p, key):
+        s, a = tl.sort(p), tl.argsort(p)
+        return (t,) + tuple(s) + tuple(a)
+    tr = T.trace_item(item, [("f32", 5), "key"], 2, {})
+    nan = np.float32(np.nan)
+    p = np.float32([[3.0, 1.0, 2.0, 1.0, -5.0], [nan, 0.0, -0.0, 2.0, nan], [4.0, 3.0, 2.0, 1.0, 0.0],
+                    [1.0, 1.0, 1.0, 1.0, 1.0]])
+    r = Evaluator(tr, 1).run([p, prng.split(prng.PRNGKey(0), len(p))], [])["results"]
+    got_s = np.stack(r[:5], 1).astype(np.float32)
+    got_a = np.stack(r[5:], 1)
+    want_a = np.argsort(p, axis=1, kind="stable")
+    assert np.array_equal(got_a, want_a)
+    want_s = np.take_along_axis(p, want_a, 1)
+    assert np.array_equal(got_s.view(np.uint32)[~np.isnan(got_s)], want_s.view(np.uint32)[~np.isnan(want_s)])
+    assert np.array_equal(np.isnan(got_s), np.isnan(want_s))
