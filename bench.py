@@ -252,6 +252,44 @@ def oracle_step(cfg, host, n, nth):
         oracle.ph_grad(host[0][:n], nthreads=nth, libm=True)
 
 
+def oracle_check(cfg, pre, nth):
+    """the oracle in its checker mode (the backend's shared math, f64 tally partials) on the items `pre` -> dict with
+    the per-item k and trunc"""
+    from oracle import oracle
+    if cfg.name == "rw":
+        return oracle.rw_fwd(pre[0], pre[1], 1.0, max_steps=cfg.max_steps, nthreads=nth)
+    if cfg.name == "q1":
+        return oracle.q1_fwd(pre[0], pre[1], 2.0, max_steps=cfg.max_steps, nthreads=nth)
+    if cfg.name == "ph":
+        return oracle.ph_fwd(pre[0], max_steps=cfg.max_steps, nthreads=nth)
+    if cfg.name == "od":
+        return oracle.od_fwd(*pre, max_steps=cfg.max_steps, nthreads=nth)
+    return oracle.sh_fwd(*pre, max_steps=cfg.max_steps, nthreads=nth)
+
+
+def parity_block(cfg, host, runs, nth, prefix=262144, longest=1024):
+    """Per-item parity of the timed launches against the oracle: the first `prefix` items and the `longest` items
+    with the most steps (gathered by index: the heavy tail near max_steps), per-item trip counts and truncation
+    flags bitwise.  runs: {launch name: (k, trunc) host arrays of the whole launch}.  Items are independent, so a
+    prefix or a gathered subset has the same per-item results as the whole launch."""
+    N = len(host[0])
+    k0 = next(iter(runs.values()))[0]
+    tail = np.sort(np.argsort(k0, kind="stable")[::-1][:min(longest, N)])
+    idx = np.union1d(np.arange(min(prefix, N)), tail)
+    t0 = time.perf_counter()
+    ref = oracle_check(cfg, [np.ascontiguousarray(h[idx]) for h in host], nth)
+    out = {"items": int(len(idx)), "of": N, "prefix": int(min(prefix, N)), "longest": int(len(tail)),
+           "max_steps_compared": int(ref["k"].max()) if len(idx) else 0,
+           "truncated_compared": int(ref["trunc"].sum()),
+           "checker": "oracle/ (shared f32 math, f64 tally partials)", "host_s": None}
+    for name, (k, tr) in runs.items():
+        out[name] = {"k_bitwise": bool(np.array_equal(k[idx], ref["k"])),
+                     "trunc_bitwise": bool(np.array_equal(tr[idx].astype(bool), ref["trunc"]))}
+    out["host_s"] = round(time.perf_counter() - t0, 1)
+    out["ok"] = all(v["k_bitwise"] and v["trunc_bitwise"] for v in out.values() if isinstance(v, dict))
+    return out
+
+
 def cpu_rate(cfg, host, target_s, nth):
     """-> (items, seconds, Mitems/s) of oracle_step on a prefix of the items sized to about target_s seconds"""
     n = min(4096, len(host[0]))
@@ -273,6 +311,7 @@ def main():
     ap.add_argument("--config", default="rw", choices=["rw", "ph", "q1", "od", "sh"])
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the per-item parity check against the oracle")
     ap.add_argument("--unfused", action="store_true", help="time the step as a forward and a replay launch")
     ap.add_argument("--exact-order", action="store_true",
                     help="time the fused replay (the reverse program's summation order, bitwise) instead of the "
@@ -517,6 +556,17 @@ def main():
                            "frac": round(gbs / hbm, 5) if hbm else None,
                            "peak_source": "measured: MEASURED_PEAKS.json hbm_gbs" if hbm else None}
 
+    parity = None
+    if rank == 0 and not args.no_parity:
+        # the timed launches' per-item outputs (this rank's items) against the oracle on a prefix + the longest items
+        runs = {"forward": (kk, fo[fnames.index("truncated")].to("cpu").numpy())}
+        if fused is not None and not sh_vg:
+            runs["value_and_grad"] = (vo[vnames.index("k")].to("cpu").numpy(),
+                                      vo[vnames.index("truncated")].to("cpu").numpy())
+        elif sh_vg:
+            runs["value_and_grad"] = (r_last["k"].to("cpu").numpy(), r_last["trunc"].to("cpu").numpy())
+        parity = parity_block(cfg, host, runs, len(os.sched_getaffinity(0)))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nth = len(os.sched_getaffinity(0))
@@ -557,6 +607,8 @@ def main():
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if parity is not None:
+        line["parity"] = parity
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

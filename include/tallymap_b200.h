@@ -109,8 +109,10 @@ int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64
  * library instead, at most 65,536 bins (2.75 MiB, held by every GPU that loads the library until the process exits);
  * a larger n_bins is rejected with TM_EINVAL.  The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.  Each call clears
- * the words it uses, so consecutive calls are independent, but every call shares the one array: calls that can
- * overlap on the GPU (other streams, other host threads) race and must be serialised by the caller.
+ * the words it uses, so consecutive calls are independent, but every call on a device shares that device's copy of
+ * the array: calls on one device that can overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller (calls on different devices do not race).  The looked-up address lives as long as the
+ * device's primary context: after cudaDeviceReset of that device, do not call this entry point again in the process.
  * (No counterpart in the reference: its handler receives every scratch buffer from XLA.) */
 int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins,
                              float* out, int32_t* stats);

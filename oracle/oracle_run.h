@@ -58,7 +58,15 @@ i64 checkpointed_while(const P& prog, const S& init, int C, A& adj, S* final, Po
     post(c, adj);
     return K;
   }
-  std::vector<S> head(C + 1), ck(C), tape(C);
+  // the head, checkpoint and tape buffers are per host thread and reused across items (only their first slots up
+  // to what an item writes are read), so a large C -- which makes the replay linear in K, bitwise the same
+  // cotangents as any other C -- costs no per-item allocation
+  thread_local std::vector<S> head, ck, tape;
+  if (head.size() < (size_t)C + 1) {
+    head.resize(C + 1);
+    ck.resize(C);
+    tape.resize(C);
+  }
   S c = init;
   i64 K = 0;
   while (prog.cond(c)) {                       // count pass: head slot min(k, C) (slot C: scratch sink)

@@ -49,20 +49,7 @@ __global__ void exact_scatter_kernel(const float* vals, const i32* bins, long lo
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const i32 b = bins[i];
     if ((u32)b >= (u32)n_bins) { atomicAdd(&stats[kStDroppedEmits], 1); continue; }
-    const float v = vals[i];
-    const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
-    bool bad = e == 255u;
-    if (!bad) {
-      const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
-      if (m) {
-        const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
-        const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull), hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
-        const bool neg = (bits >> 31) != 0u;
-        u64* const a = words + (long long)b * kExactWords;
-        if (lo) bad = exact_add_word(a, (int)j, neg ? -lo : lo) || bad;
-        if (hi) bad = exact_add_word(a, (int)j + 1, neg ? -hi : hi) || bad;
-      }
-    }
+    const bool bad = exact_emit_atomic(words + (long long)b * kExactWords, vals[i]);
     if (bad) { atomicAdd(&stats[kStFixedPointOverflow], 1); atomicOr(&flags[b], 1u); }
   }
 }

@@ -172,7 +172,10 @@ int occupancy(Kernel& k, int dev, int* occ) {
 // Scratch of tm_exact_scatter_noalloc: the exact words of at most TM_NOALLOC_MAX_BINS bins, in a fixed device array
 // that every GPU loading this library holds until the process exits (2.75 MiB).  Host code must not pass the array's
 // name to a kernel (on the host it is a stand-in, not a device address): noalloc_words() looks up its device address
-// once per device, with that device current, and caches it.
+// once per device, with that device current, and caches it.  Each device holds its own copy of the array, so the
+// cached address belongs to that device's primary context: it stays valid until the process exits, unless the
+// process calls cudaDeviceReset on that device, which destroys the context and the array with it (after such a reset
+// this entry point must not be called again in the process).
 #define TM_NOALLOC_MAX_BINS 65536
 static __device__ __align__(256) unsigned long long
     g_noalloc_words[(size_t)TM_NOALLOC_MAX_BINS * tmb::kExactWords + (TM_NOALLOC_MAX_BINS + 1) / 2];
@@ -461,8 +464,9 @@ int tm_exact_scatter(void* stream, const float* vals, const int32_t* bins, int64
 
 // The exact scatter-add of tm_exact_scatter without a caller-provided scratch buffer and without allocating: for
 // callers that cannot call cudaMalloc (see the header).  Clears the words it needs, then runs the same two kernels on
-// the same stream.  The fixed scratch is shared by every call in the process, so calls whose work overlaps on the
-// GPU (different streams, or devices sharing nothing but the call order) race on it; serialise them.
+// the same stream.  Every device has its own copy of the fixed scratch, shared by every call on that device: calls on
+// one device whose work can overlap on the GPU (other streams, other host threads) race on it and must be
+// serialised by the caller; calls on different devices do not race.
 int tm_exact_scatter_noalloc(void* stream, const float* vals, const int32_t* bins, int64_t n, int32_t n_bins,
                              float* out, int32_t* stats) {
   if ((n > 0 && (!vals || !bins)) || !out || !stats || n < 0 || n_bins < 1)

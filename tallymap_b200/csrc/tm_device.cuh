@@ -1,8 +1,9 @@
 // Device primitives of the tallymap B200 runtime: scalar types, the kernel parameter block, jax.random's
 // threefry2x32 draws, float->int conversion, the subnormal-safe f32 atomic add and the exact f32 sum.
 //
-// Semantics follow the reference's generated PRELUDE (tallymap/backends/kernel/kernel.py:26-188) and its DENSE
-// accumulator (kernel.py:870-941); the code is written for sm_100a.  All product kernels are compiled with
+// Semantics follow the reference's generated PRELUDE (tallymap/backends/kernel/kernel.py:26-188) and the word format of
+// its DENSE accumulator (kernel.py:870-941; the arithmetic on it is this build's own, tm_exact.h); the code is
+// written for sm_100a.  All product kernels are compiled with
 // --fmad=false, so every f32 + - * below is one IEEE rounding, as the reference's NVRTC flags (-fmad=false,
 // backends/kernel/compile.py:27) and its host target (-ffp-contract=off) make it.
 #pragma once
@@ -11,6 +12,7 @@
 #else
 #include <cstdint>
 #endif
+#include "tm_exact.h"
 
 namespace tmb {
 
@@ -127,66 +129,53 @@ __device__ __forceinline__ void fatom(float* a, float v) {
 }
 
 // ------------------------------------------------------------------------------------------------ exact f32 sum
-// A bin keeps the exact sum of its f32 emits as an integer in units of 2^-149, in kExactWords signed int64 words of
-// weight 2^(63 j) (kernel.py:870-941).  An add into word j that overflows int64 carries +-2 into word j+1; a carry
-// out of the top word returns true and the caller flags the bin (NaN at readout), so a bin is exact or NaN.
-constexpr int kExactWords = 5;
+// A bin keeps the exact sum of its f32 emits in kExactWords signed 64-bit words of weight 2^(63 j) units of 2^-149
+// (the format and its host/device arithmetic: tm_exact.h).  Here: the device's atomic forms and thread-private words.
+constexpr int kExactWords = tmx::kWords;
 
-__device__ __noinline__ bool exact_carry(u64* a, int j, i64 c) {   // the rare +-2 carry into word j
-  for (; j < kExactWords; ++j) {
-    const i64 o = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)c);
-    const i64 r = (i64)((u64)o + (u64)c);
-    if (!((c > 0 && r < o) || (c < 0 && r > o))) return false;
+// the rare carry of an atomic add: c (+-2) into word j and upward, one atomic per word; true if it leaves the top
+// word (kept out of line: it almost never runs, and inlined it would hold registers in every emitting loop)
+__device__ __noinline__ bool exact_atomic_ripple(u64* a, int j, i64 c) {
+  for (; c != 0; ++j) {
+    if (j >= kExactWords) return true;
+    i64 old = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)c);
+    c = tmx::add_wrap(old, c);
   }
-  return true;
-}
-
-__device__ __forceinline__ bool exact_add_word(u64* a, int j, i64 q) {
-  const i64 o = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)q);
-  const i64 r = (i64)((u64)o + (u64)q);
-  if (q > 0 && r < o) return exact_carry(a, j + 1, 2);
-  if (q < 0 && r > o) return exact_carry(a, j + 1, -2);
   return false;
 }
 
-// A thread-private exact accumulator of NB bins in registers: per-item cotangents are added here without atomics,
-// and each thread adds its words into the block's shared words once, when it runs out of items.  Integer addition
-// is associative, so where a value is added first does not change the total: the readout is bitwise the same as
-// adding every emit straight into the global bin.
-// Word j0 of bin b of a thread's private words += q (non-atomic), carries rippling upward: word(b, j) gives word j of
-// bin b (an i64 lvalue).  True if a carry leaves the top word.
-template <class Word>
-__device__ __forceinline__ bool exact_priv_add(Word&& word, int b, int j0, i64 q) {
-#pragma unroll
-  for (int jj = 0; jj < kExactWords; ++jj) {
-    if (jj < j0 || q == 0) continue;
-    i64& w = word(b, jj);
-    const i64 o = w;
-    const i64 r = (i64)((u64)o + (u64)q);
-    w = r;
-    q = (q > 0 && r < o) ? 2 : ((q < 0 && r > o) ? -2 : 0);
-    j0 = jj + 1;
-  }
-  return q != 0;
+// word j of the bin at a += q with one atomic; a wrap of that word (detected from the value the atomic returned)
+// carries into the words above.  True if a carry left the top word.
+__device__ __forceinline__ bool exact_add_word(u64* a, int j, i64 q) {
+  i64 old = (i64)atomicAdd((unsigned long long*)&a[j], (unsigned long long)q);
+  const i64 c = tmx::add_wrap(old, q);
+  return c != 0 && exact_atomic_ripple(a, j + 1, c);
 }
 
-// The carry-save add of one f32 into bin b of a thread's private words; flag: the bins' flag bits.  Returns true
-// when the bin must be flagged (non-finite, or a carry lost).
+// one f32 into the bin at a with atomics; true when the bin must be flagged (non-finite v, or a carry lost)
+__device__ __forceinline__ bool exact_emit_atomic(u64* a, float v) {
+  const tmx::Addend d = tmx::addend(v);
+  if (d.nonfinite) return true;
+  bool lost = false;
+  if (d.s0) lost = exact_add_word(a, d.j, d.s0);
+  if (d.s1) lost = exact_add_word(a, d.j + 1, d.s1) || lost;
+  return lost;
+}
+
+// Thread-private words (no atomics): word(b, j) gives word j of bin b as an i64 lvalue.  Integer addition is
+// associative, so adding per-item values here first and the thread's words into a shared or global bin later reads
+// out bitwise the same as adding every emit straight into the bin.
+template <class Word>
+__device__ __forceinline__ bool exact_priv_add(Word&& word, int b, int j, i64 q) {
+  return tmx::add_at([&word, b](int jj) -> i64& { return word(b, jj); }, j, q);
+}
+
+// one f32 into bin b of a thread's private words; flag: the bins' flag bits.  True when the bin must be flagged.
 template <class Word>
 __device__ __forceinline__ bool exact_priv_emit(Word&& word, u32& flag, int b, float v) {
-  const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
-  if (e == 255u) { flag |= 1u << b; return true; }
-  const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
-  if (m == 0ull) return false;
-  const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
-  const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
-  const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;
-  const bool neg = (bits >> 31) != 0u;
-  bool lost = false;
-  if (lo) lost = exact_priv_add(word, b, (int)j, neg ? -lo : lo);
-  if (hi) lost = exact_priv_add(word, b, (int)j + 1, neg ? -hi : hi) || lost;
-  if (lost) flag |= 1u << b;
-  return lost;
+  const bool bad = tmx::add_float([&word, b](int jj) -> i64& { return word(b, jj); }, v);
+  if (bad) flag |= 1u << b;
+  return bad;
 }
 
 template <int NB>
@@ -220,43 +209,12 @@ __device__ __forceinline__ bool exact_merge_bin(u64* dst, const i64* src) {
   return lost;
 }
 
-// The correctly rounded (nearest, ties to even) f32 of sum_j a[j] 2^(63 j) 2^-149: the words are summed into a
-// 384-bit two's complement integer, its magnitude's top 64 bits plus a sticky bit are rounded once to 24 bits.
-// *bad: the total overflows f32.
+// the correctly rounded f32 of a bin's words (tmx::read); *bad: the total overflows f32
 __device__ __noinline__ float exact_read(const u64* a, bool* bad) {
-  u64 d[6] = {0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
-  for (int j = 0; j < kExactWords; ++j) {
-    const i64 w = (i64)a[j];
-    const int sh = 63 * j, limb = sh >> 6, bit = sh & 63;
-    const u64 ext = w < 0 ? ~0ull : 0ull;
-    const u64 lo = (u64)w << bit, hi = bit ? (u64)(w >> (64 - bit)) : ext;
-    u64 c = 0ull;
-    for (int k = limb; k < 6; ++k) {
-      const u64 y = (k == limb) ? lo : (k == limb + 1 ? hi : ext);
-      const u64 t = d[k] + y, u = t + c;
-      c = (t < y ? 1ull : 0ull) + (u < t ? 1ull : 0ull);
-      d[k] = u;
-    }
-  }
-  const bool neg = (i64)d[5] < 0;
-  if (neg) {
-    u64 c = 1ull;
-    for (int k = 0; k < 6; ++k) { d[k] = ~d[k] + c; c = (c && d[k] == 0ull) ? 1ull : 0ull; }
-  }
-  int t = 5;
-  while (t >= 0 && d[t] == 0ull) --t;
-  if (t < 0) return 0.0f;
-  const int lz = __clzll((long long)d[t]);
-  const u64 below = t >= 1 ? d[t - 1] : 0ull;
-  const u64 top = lz ? (d[t] << lz) | (below >> (64 - lz)) : d[t];
-  bool sticky = lz ? (below << lz) != 0ull : below != 0ull;
-  for (int j = 0; j < t - 1; ++j) sticky = sticky || d[j] != 0ull;
-  u64 q = top >> 40;
-  const u64 rem = top & 0xffffffffffull, half = 0x8000000000ull;
-  if (rem > half || (rem == half && (sticky || (q & 1ull)))) ++q;
-  const float o = (float)ldexp((double)q, 64 * t + 40 - lz - 149);
-  if (!(fabs((double)o) <= 3.4028234663852886e38)) *bad = true;
-  return neg ? -o : o;
+  i64 w[kExactWords];
+#pragma unroll
+  for (int j = 0; j < kExactWords; ++j) w[j] = (i64)a[j];
+  return tmx::read(w, bad);
 }
 
 }  // namespace tmb

@@ -79,21 +79,7 @@ struct ExactPrivS {
 // bin's carry-save words (atomics, on shared or global words), so the bin is the correctly rounded f32 of the exact
 // sum whatever the order of the emits.  A non-finite emit or a carry out of the top word flags the bin (NaN at
 // readout), counted in stats[3]; an index outside [0, S) is dropped and counted in stats[4].
-__device__ __forceinline__ bool exact_emit_atomic(u64* w, float v) {
-  const u32 bits = __float_as_uint(v), e = (bits >> 23) & 255u;
-  if (e == 255u) return true;
-  const u64 m = (u64)(bits & 0x7fffffu) | (e ? 0x800000ull : 0ull);
-  if (m == 0ull) return false;
-  const u32 p = e ? e - 1u : 0u, j = p / 63u, s = p - 63u * j;
-  const i64 lo = (i64)((m << s) & 0x7fffffffffffffffull);
-  const i64 hi = s >= 40u ? (i64)(m >> (63u - s)) : 0;   // (s >= 40 only for j <= 3: j + 1 is a word)
-  const bool neg = (bits >> 31) != 0u;
-  bool lost = false;
-  if (lo) lost = exact_add_word(w, (int)j, neg ? -lo : lo);
-  if (hi) lost = exact_add_word(w, (int)j + 1, neg ? -hi : hi) || lost;
-  return lost;
-}
-
+// (exact_emit_atomic: tm_device.cuh)
 template <int S>
 struct ExactSum {
   // words: S x 5 u64, then S u32 flags (shared or global); bytes of that layout

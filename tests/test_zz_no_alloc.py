@@ -50,6 +50,9 @@ def test_noalloc_matches_scratch_entry_point_twice(cuda, tmlib):
         out, st, ref, ref_st = run_both(tmlib, vals, bins, nb)
         assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
         assert np.array_equal(st, ref_st)
+    # and the first call's bins against the golden known answers themselves (the integer reference, rounded once)
+    out, st, _, _ = run_both(tmlib, d["wide_vals"], d["wide_bins"], int(d["wide_nb"]))
+    assert np.array_equal(out.view(np.uint32), d["wide_expect"].view(np.uint32))
 
 
 def test_noalloc_rejects_more_bins_than_its_scratch(tmlib):
