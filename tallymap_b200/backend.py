@@ -386,7 +386,11 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
     alloc_results), reused without reallocation.  order: optional int32[N] permutation, the order in which the
     kernel's threads claim items (e.g. longest first, from a primal call's trip counts); it changes no result.
     n_active: optional item count <= N (the reference's n_active, _api.py:466-469): only items i < n_active run; the
-    others emit nothing, are never truncated and their per-item results are zero (the launch zeroes them)."""
+    others emit nothing, are never truncated and their per-item results are zero (the launch zeroes them); refused
+    for a spawning program, as the reference refuses it (_api.py:530-532: a child's item index would reach beyond
+    the active count)."""
+    if n_active is not None and p.spawns:
+        raise ValueError("tallymap: n_active with spawn is not supported")
     if target != "cuda":
         raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
     if not torch.cuda.is_available():

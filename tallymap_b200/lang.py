@@ -582,7 +582,8 @@ def _sorted_pairs(xs):
     for p in range(n):
         for j in range(p % 2, n - 1, 2):
             a, b = v[j], v[j + 1]
-            swap = (b < a) | ((a != a) & (b == b)) if isinstance(a, T.Var) and a.dtype == T.F32 else (b < a)
+            flt = any((isinstance(z, T.Var) and z.dtype == T.F32) or isinstance(z, float) for z in (a, b))
+            swap = (b < a) | ((a != a) & (b == b)) if flt else (b < a)
             v[j], v[j + 1] = where(swap, b, a), where(swap, a, b)
             idx[j], idx[j + 1] = where(swap, idx[j + 1], idx[j]), where(swap, idx[j], idx[j + 1])
     return T.Vec(v), T.Vec(idx)
@@ -745,7 +746,7 @@ class random:
     @staticmethod
     def randint(key, shape=(), minval=0, maxval=2):
         """jax.random.randint for int32 Python-int bounds: two 32-bit draws from split(key) combined modulo the
-        span (2^32 mod span folded in through its square root), minval where maxval <= minval"""
+        span with jax's uint32 arithmetic (every product wraps modulo 2^32), minval where maxval <= minval"""
         if not (isinstance(minval, int) and isinstance(maxval, int)):
             raise T.UnsupportedError("tallymap_b200.lang.random.randint: Python int bounds only")
         import builtins
@@ -757,8 +758,10 @@ class random:
             span = (span + 1) & 0xFFFFFFFF
         k1, k2 = random.split(key)
         hb, lb = random.bits(k1, shape), random.bits(k2, shape)
+        # jax forms the multiplier 2^32 mod span in uint32: (2^16 mod span)^2 wraps modulo 2^32 before its remainder
+        # (lax.mul on uint32), so for a span above 2^16 the square is 2^32 -> 0 and the multiplier is 0
         mult = (2 ** 16) % span if span else 0
-        mult = (mult * mult) % span if span else 0
+        mult = ((mult * mult) & 0xFFFFFFFF) % span if span else 0
 
         def one(h, l):
             off = (h % span) * mult + (l % span)

@@ -710,12 +710,13 @@ def test_randint_gumbel_categorical():
 
     def item(t, key):
         return (t, tl.random.randint(key, (), -3, 10), tl.random.randint(key, (2,), 5, 5)[1],
-                tl.random.categorical(key, tl.array([0.0, 1.0, -1.0, 0.5])), tl.random.gumbel(key))
+                tl.random.categorical(key, tl.array([0.0, 1.0, -1.0, 0.5])), tl.random.gumbel(key),
+                tl.random.randint(key, (), 0, 100000), tl.random.randint(key, (), -70000, 2 ** 31 - 1))
     tr = T.trace_item(item, ["key"], 1, {})
     n = 4000
     keys = prng.split(prng.PRNGKey(21), n)
     r = Evaluator(tr, 1).run([keys], [])["results"]
-    ri, same, cat, g = r
+    ri, same, cat, g, big, huge = r
     assert ri.min() == -3 and ri.max() == 9 and (same == 5).all()
     k1 = np.array([prng.threefry2x32(np.uint32(k[0]), np.uint32(k[1]), np.uint32(0), np.uint32(0)) for k in keys])
     k2 = np.array([prng.threefry2x32(np.uint32(k[0]), np.uint32(k[1]), np.uint32(0), np.uint32(1)) for k in keys])
@@ -725,6 +726,13 @@ def test_randint_gumbel_categorical():
     mult = (65536 % span) ** 2 % span
     want = (((bits(k1) % span) * mult + bits(k2) % span) % (2 ** 32) % span).astype(np.int64) - 3
     assert np.array_equal(ri, want)
+    # spans above 2^16: jax's multiplier (2^16 mod span)^2 mod span is formed in uint32, where the square wraps
+    for span, lo, got in ((100000, 0, big), (2 ** 31 - 1 + 70000, -70000, huge)):
+        m32 = (((65536 % span) ** 2) & 0xFFFFFFFF) % span
+        want = ((((bits(k1) % span) * m32) & 0xFFFFFFFF) + bits(k2) % span) & 0xFFFFFFFF
+        want = (want % span).astype(np.int64) + lo
+        assert np.array_equal(got.astype(np.int64), want)
+    assert (((65536 % 100000) ** 2) & 0xFFFFFFFF) % 100000 == 0      # the wrap that an exact product would miss
     p = np.exp([0.0, 1.0, -1.0, 0.5])
     p /= p.sum()
     freq = np.bincount(cat, minlength=4) / n
@@ -840,6 +848,14 @@ def test_interp_and_table_search():
     assert np.array_equal(r[3], np.where(x < 0, np.float32(-9), want))
 
 
+def test_n_active_with_spawn_is_refused():
+    """n_active with a spawning program raises, as the reference's mapped call does (_api.py:530-532)"""
+    from tallymap_b200 import backend as B
+    E, d, k = np.ones(4, np.float32), np.zeros(4, np.float32), prng.split(prng.PRNGKey(0), 4)
+    with pytest.raises(ValueError, match="n_active with spawn is not supported"):
+        B.run(B.SH_FWD, [E, d, k], [np.float32(1.0)], consts=(100,), n_active=2)
+
+
 def test_sort_argsort():
     """sort / argsort of a vector (a sorting network of compare-exchanges): ascending, NaNs last, stable (numpy's
     stable sort on the same values, the signed zeros kept in their input order)"""
@@ -860,3 +876,19 @@ def test_sort_argsort():
     want_s = np.take_along_axis(p, want_a, 1)
     assert np.array_equal(got_s.view(np.uint32)[~np.isnan(got_s)], want_s.view(np.uint32)[~np.isnan(want_s)])
     assert np.array_equal(np.isnan(got_s), np.isnan(want_s))
+
+    # a vector mixing Python-float constants with traced values: NaNs last whichever side holds the constant
+    def mixed(t, p, key):
+        v = tl.array([2.0, p[0], 0.5, p[1], float("nan"), p[2]])
+        s, a = tl.sort(v), tl.argsort(v)
+        return (t,) + tuple(s) + tuple(a)
+    tr = T.trace_item(mixed, [("f32", 3), "key"], 2, {})
+    q = np.float32([[nan, 1.0, 3.0], [-1.0, nan, nan], [0.5, 0.5, -0.0]])
+    r = Evaluator(tr, 1).run([q, prng.split(prng.PRNGKey(0), len(q))], [])["results"]
+    full = np.float32([[2.0, a, 0.5, b, nan, c] for a, b, c in q])
+    want_a = np.argsort(full, axis=1, kind="stable")
+    assert np.array_equal(np.stack(r[6:], 1), want_a)
+    got_s = np.stack(r[:6], 1).astype(np.float32)
+    want_s = np.take_along_axis(full, want_a, 1)
+    assert np.array_equal(np.isnan(got_s), np.isnan(want_s))
+    assert np.array_equal(got_s[~np.isnan(got_s)].view(np.uint32), want_s[~np.isnan(want_s)].view(np.uint32))
