@@ -128,6 +128,44 @@ def configs(B):
 FAM = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz", "sh": "shower"}
 
 
+OD_FP32_OPS = 255     # f32 add / mul / min / max / abs / compare of one Lorenz RK45 trial step (+ 3 div, 1 sqrt, 1 pow)
+
+
+def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_kernel):
+    """The Lorenz ensemble's roofline: its bound is the issue rate of its own instruction mix (six stage
+    evaluations, the error norm, an f32 pow in the shared double-precision math, the accept decision), so the peaks
+    are tm_probe_issue's probes of that mix at full occupancy: P0 trial steps/s (kind 2) and P1 (trial step + step
+    VJP)/s (kind 3).  The forward runs `steps` trial steps; the replay `micro` forward step evaluations (count,
+    checkpoint and fill passes) and one step VJP per trial step.  Ideal times: forward steps / P0; replay
+    steps / P1 + (micro - steps) / P0.  achieved is in forward-step equivalents (a VJP pair counts P0 / P1), so
+    frac = ideal time / measured time.  Beside it the FP32 pipe: the trial steps' algorithmic f32 operations over
+    the forward time against the probe's FP32 instruction rate (kind 1)."""
+    p0, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP, 512, stream, dev)
+    p1, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP_VJP, 256, stream, dev)
+    pf, _ = _lib.probe_rate(_lib.PROBE_FP32, 8192, stream, dev)
+    pf *= 16
+    g_s, f_s = g_ms / 1e3, f_ms / 1e3
+    ideal_g = steps / p1 + max(micro - steps, 0) / p0
+    ideal_f = steps / p0
+    eq = ideal_g * p0
+    return {"bound": "issue", "kernel": grad_kernel, "achieved": round(eq / g_s / 1e9, 4), "peak": round(p0 / 1e9, 4),
+            "unit": "G trial-step equivalents/s", "frac": round(ideal_g / g_s, 4), "traffic": None,
+            "peak_source": "measured: tm_probe_issue kind 2 (the item's trial step at full occupancy, no "
+                           "divergence or memory) and kind 3 (trial step + step VJP) on this GPU",
+            "work": f"{steps} trial steps (accepted + rejected) and {micro} forward step evaluations of the replay "
+                    f"(count, checkpoint, fill), one step VJP per trial step",
+            "probe": {"p0_steps_per_s": round(p0, 1), "p1_step_vjp_per_s": round(p1, 1)},
+            "modes": {"fwd": {"kernel": fwd_kernel, "achieved": round(steps / f_s / 1e9, 4),
+                              "frac": round(ideal_f / f_s, 4)},
+                      "grad": {"kernel": grad_kernel, "achieved": round(eq / g_s / 1e9, 4),
+                               "frac": round(ideal_g / g_s, 4)},
+                      "step": {"frac": round((ideal_f + ideal_g) / (f_s + g_s), 4)}},
+            "fp32": {"ops_per_trial_step": OD_FP32_OPS, "kernel": fwd_kernel,
+                     "achieved_tops": round(steps * OD_FP32_OPS / f_s / 1e12, 3), "peak_tops": round(pf / 1e12, 3),
+                     "frac": round(steps * OD_FP32_OPS / f_s / pf, 4),
+                     "peak_source": "measured: tm_probe_issue kind 1 (independent f32 multiply and add chains)"}}
+
+
 def replay_micro_steps(K, C):
     """loop-step evaluations of the checkpointed replay (count, checkpoint, advance + fill, sweep) for trip counts K,
     summed: the schedule of tallymap/_reverse.py:343-440."""
@@ -539,7 +577,10 @@ def main():
                         (f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
                          f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
                          "steps from the per-item trip counts and the replay schedule)")} if (cfg.tf or sh_vg) else None
-    if roofline is not None and not tree:
+    if cfg.name == "od":
+        roofline = od_roofline(_lib, stream, dev, steps_total, replay_micro_steps(kk, C_used), f_ms, g_ms,
+                               cfg.grad.kernel, cfg.fwd.kernel)
+    if roofline is not None and not tree and cfg.name != "od":
         # per mode (the separate launches): the forward and the replay gradient against the same probe
         roofline["modes"] = {
             "fwd": {"kernel": cfg.fwd.kernel, "achieved": round(tf_fwd / (f_ms / 1e3) / 1e9, 2),

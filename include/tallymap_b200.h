@@ -137,6 +137,16 @@ int tm_tree_generations(void* stream, const void* records, int64_t n_records, in
  * (No counterpart in the reference, which reports no rooflines.) */
 int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_len, int64_t* threads_used);
 
+/* Issue-rate probes for rooflines, launched like tm_probe_threefry on every resident thread slot (at most out_len
+ * threads), `iters` iterations per thread, register-resident, no memory traffic besides one word per thread:
+ *   kind 0  one threefry2x32 per iteration (the walkers' dominant operation; = tm_probe_threefry)
+ *   kind 1  16 FP32 instructions per iteration (8 independent multiply and add chains): the FP32 issue rate
+ *   kind 2  one trial step of the Lorenz RK45 item per iteration (its own instruction mix at its own occupancy)
+ *   kind 3  one trial step and one step VJP of that item per iteration (the replay's sweep mix)
+ * (No counterpart in the reference, which reports no rooflines.) */
+int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
+                   int64_t* threads_used);
+
 /* The backend's f32 math on the device, elementwise: fn 0 log, 1 exp, 2 sin, 3 cos, 4 pow(x, y), 5 atan,
  * 6 atan2(x, y) (x the ordinate), 7 asin, 8 acos, 9 tan, 10 sinh, 11 cosh, 12 asinh, 13 acosh, 14 atanh, 15 exp2,
  * 16 log2, 17 cbrt, 18 erf, 19 erfc, 20 erfinv (y read only by pow and atan2).

@@ -93,6 +93,7 @@ def lib():
         L.tm_exact_scatter_noalloc.argtypes = [P, P, P, i64, i32, P, P]
         L.tm_math_eval.argtypes = [P, i32, P, P, P, i64]
         L.tm_probe_threefry.argtypes = [P, i32, P, i64, ctypes.POINTER(i64)]
+        L.tm_probe_issue.argtypes = [P, i32, i32, P, i64, ctypes.POINTER(i64)]
         L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, i32, P, P, P]
         L.tm_compile_register.argtypes = [i64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]
         L.tm_compile.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, i32, P, ctypes.c_size_t,
@@ -109,8 +110,30 @@ def check(rc):
 # the symbols include/tallymap_b200.h declares (tests check the library exports each one)
 EXPORTS = ("tm_abi_version", "tm_last_error", "tm_kernel_id", "tm_kernel_name", "tm_register", "tm_kernel_info",
            "tm_launch", "tm_check_status", "tm_exact_combine", "tm_exact_scatter", "tm_exact_scatter_noalloc",
-           "tm_probe_threefry", "tm_math_eval", "tm_tree_generations",
+           "tm_probe_threefry", "tm_probe_issue", "tm_math_eval", "tm_tree_generations",
            "tm_compile_register", "tm_compile")
+
+
+PROBE_THREEFRY, PROBE_FP32, PROBE_ODE_STEP, PROBE_ODE_STEP_VJP = 0, 1, 2, 3
+
+
+def probe_rate(kind, iters, stream, device, reps=3):
+    """iterations per second of tm_probe_issue's probe `kind` at full occupancy on `device` (CUDA events on
+    `stream`, the best of `reps` launches) -> (rate, threads)"""
+    import torch
+    out = torch.empty(148 * 2048 * 2, dtype=torch.int32, device=device)
+    used = ctypes.c_int64()
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        check(lib().tm_probe_issue(ctypes.c_void_p(stream.cuda_stream), kind, iters, ctypes.c_void_p(out.data_ptr()),
+                                   out.numel(), ctypes.byref(used)))
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    return used.value * iters / (best / 1e3), used.value
 
 
 def kernel_id(name):

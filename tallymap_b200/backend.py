@@ -624,8 +624,18 @@ def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None,
         replay_bytes = replay_plan(p, max_steps or 2 ** 31 - 1, None, device)[2]
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
     R = record_capacity(N, record, device) if p.record_bytes else 0
-    layout, _ = p.result_layout(N, replay_bytes or 0, Q, R)
-    return [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout]
+    layout, n_zero = p.result_layout(N, replay_bytes or 0, Q, R)
+    # the zeroed results (tallies, scratch accumulators, control words, stats) share ONE allocation, each at a
+    # 16-byte aligned offset in layout order: Sum tallies of one dtype that follow each other in the layout are then
+    # one contiguous range, which the multi-GPU step all_reduces in place with no packing copy
+    # (parallel.all_reduce_sums)
+    offs, o = [], 0
+    for _, nb, _, _ in layout[:n_zero]:
+        offs.append(o)
+        o += (nb + 15) // 16 * 16
+    blob = torch.empty(max(o, 16), dtype=torch.uint8, device=device)
+    out = [blob[a:a + nb].view(dt).view(shape) for a, (_, nb, dt, shape) in zip(offs, layout[:n_zero])]
+    return out + [torch.empty(shape, dtype=dt, device=device) for _, _, dt, shape in layout[n_zero:]]
 
 
 def check_status(ctl):

@@ -362,3 +362,41 @@ struct ODGrad : OdeCommon {
 };
 
 }  // namespace tmb
+
+namespace tmb {
+
+// Roofline probes of this item: `iters` iterations per thread on a register-resident state, every lane of a warp
+// taking the same path, no claims, no emits, no memory traffic besides one word per thread at the end.
+//   kVjp == 0: one trial step per iteration (advance: the six stages, the error norm, pow, the accept decision);
+//   kVjp == 1: a trial step and the step VJP at the state before it (the replay's sweep: stages recomputed, then
+//             run backwards), per iteration.
+// Each thread integrates its own Lorenz system (sigma, rho and y0 vary slightly by thread, as the ensemble's);
+// the integration window is restarted when it ends, so every iteration is a full trial step.  Each variant is its own
+// kernel, so each gets the register allocation, and so the occupancy, of its own code.  The rate at full occupancy is the issue-rate speed of light of the item's own instruction mix: the roofline's peak for the
+// forward and replay kernels, which add claims, divergence and memory traffic to the same instructions.
+template <int kVjp>
+__global__ void __launch_bounds__(TM_BLOCK) probe_ode_kernel(u32 iters, u32* out) {
+  const u32 t = blockIdx.x * blockDim.x + threadIdx.x;
+  ODGrad::Ctx c;
+  c.p = OdeCommon::P{10.0f + 1e-4f * (float)(t & 1023u), 28.0f - 1e-4f * (float)(t & 511u), 8.0f / 3.0f};
+  const V3 y0{1.0f, 1.0f, 1.0f + 1e-3f * (float)(t & 255u)};
+  OdeState st{0, 0, 0.0f, 1e-3f, y0, OdeCommon::f(c.p, y0)};
+  ODGrad::Adj a;
+  ODGrad::adj_start(c, a);
+  a.cy = V3{1.0f, 0.5f, 0.25f};
+  for (u32 i = 0; i < iters; ++i) {
+    if (kVjp) {
+      const OdeState at = st;
+      OdeCommon::advance(c.p, st);
+      ODGrad::vjp(c, at, a);
+      a.cy = V3{a.cy.x * 0.5f, a.cy.y * 0.5f, a.cy.z * 0.5f};   // (bounded: the cotangent stays finite)
+    } else {
+      OdeCommon::advance(c.p, st);
+    }
+    if (!(st.tt < OdeCommon::kT1)) st = OdeState{st.kc, st.k, 0.0f, 1e-3f, st.y, st.k1};
+  }
+  out[t] = __float_as_uint(st.y.x) ^ __float_as_uint(st.h) ^ (u32)st.k ^ __float_as_uint(a.cb) ^
+           __float_as_uint(a.cy.z);
+}
+
+}  // namespace tmb

@@ -6,6 +6,7 @@
 //                          the generation lists of a recorded spawn tree (the launch order of the tree adjoint)
 //   probe_threefry_kernel  the calibration probe of the roofline: threefry2x32 evaluations per second at full
 //                          occupancy with no memory traffic (the issue-rate peak of the walkers' dominant op mix)
+//   probe_fp32_kernel      the FP32 instruction rate (independent multiply and add chains)
 #pragma once
 #include "tm_device.cuh"
 #include "tm_math.h"
@@ -145,6 +146,24 @@ __global__ void math_eval_kernel(int fn, const float* x, const float* y, float* 
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     out[i] = tmm::eval(fn, x[i], y ? y[i] : 0.0f);
   }
+}
+
+// The FP32 instruction rate: per iteration 8 independent chains of one f32 multiply and one f32 add (separate
+// instructions: the library is built with --fmad=false, as every kernel here), 16 FP32 instructions per thread.
+__global__ void __launch_bounds__(128) probe_fp32_kernel(u32 iters, u32* out) {
+  const u32 t = blockIdx.x * blockDim.x + threadIdx.x;
+  float a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = 1.0f + 1e-7f * (float)(t + j);
+  const float m = 0.999999f, d = 1e-7f;
+  for (u32 i = 0; i < iters; ++i) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(__fmul_rn(a[j], m), d);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += a[j];
+  out[t] = __float_as_uint(s);
 }
 
 // iters independent threefry2x32 evaluations per thread, folded into one word per thread (so none is dead code)

@@ -550,6 +550,31 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
   return TM_OK;
 }
 
+int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
+                   int64_t* threads_used) {
+  if (!out || iters < 1 || out_len < 128 || kind < 0 || kind > 3)
+    return fail(TM_EINVAL, "tallymap_b200: tm_probe_issue: bad arguments");
+  const void* fn = kind == 0 ? (const void*)tmb::probe_threefry_kernel
+                 : kind == 1 ? (const void*)tmb::probe_fp32_kernel
+                 : kind == 2 ? (const void*)tmb::probe_ode_kernel<0> : (const void*)tmb::probe_ode_kernel<1>;
+  int dev = 0, sms = 0, occ = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 128, 0);
+  if (e != cudaSuccess) return cuda_fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", e);
+  long long blocks = (long long)sms * (occ < 1 ? 1 : occ);
+  if (blocks * 128 > out_len) blocks = out_len / 128;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (kind == 0) tmb::probe_threefry_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else if (kind == 1) tmb::probe_fp32_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else if (kind == 2) tmb::probe_ode_kernel<0><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else tmb::probe_ode_kernel<1><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("probe kernel", e);
+  if (threads_used) *threads_used = blocks * 128;
+  return TM_OK;
+}
+
 int tm_math_eval(void* stream, int32_t fn, const float* x, const float* y, float* out, int64_t n) {
   if (fn < 0 || fn >= tmm::kMathFns || n < 0 || (n > 0 && (!x || !out || ((fn == 4 || fn == 6) && !y))))
     return fail(TM_EINVAL, "tallymap_b200: tm_math_eval: bad arguments");

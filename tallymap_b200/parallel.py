@@ -25,13 +25,33 @@ def shard(n_total, rank, world):
     return start, (n_total - start if rank == world - 1 else per)
 
 
+def contiguous_span(group):
+    """one flat view over tensors of one dtype that lie back to back in one storage (in the given order), or None.
+    backend.alloc_results places a program's tallies so that those of one dtype following each other do."""
+    if not all(t.is_contiguous() for t in group):
+        return None
+    es = group[0].element_size()
+    base = group[0].untyped_storage().data_ptr()
+    for a, b in zip(group, group[1:]):
+        if b.untyped_storage().data_ptr() != base or a.data_ptr() + a.numel() * es != b.data_ptr():
+            return None
+    g0 = group[0]
+    return g0.new_empty(0).set_(g0.untyped_storage(), g0.storage_offset(), (sum(t.numel() for t in group),), (1,))
+
+
 def all_reduce_sums(tensors):
-    """in place: all_reduce(SUM) of float32 and int32 tensors, packed into one flat buffer per dtype."""
+    """in place: all_reduce(SUM) of float32 and int32 tensors, one collective per dtype.  Tensors of a dtype that
+    are one contiguous range (a single tensor, or tallies laid out back to back by backend.alloc_results) are
+    reduced in place; otherwise they are packed into a flat buffer and copied back."""
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return tensors
     for dt in (torch.float32, torch.int32):
         group = [t for t in tensors if t.dtype == dt]
         if not group:
+            continue
+        flat = contiguous_span(group)
+        if flat is not None:
+            dist.all_reduce(flat, op=dist.ReduceOp.SUM)
             continue
         flat = torch.cat([t.reshape(-1) for t in group])
         dist.all_reduce(flat, op=dist.ReduceOp.SUM)

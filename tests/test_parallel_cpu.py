@@ -63,6 +63,25 @@ def _worker(rank, world, port, mode, q):
             st = torch.arange(5, dtype=torch.int32) * (rank + 1)
             parallel.all_reduce_sums([h, c, st])
             q.put((rank, h.tolist()[:2], int(c), st.tolist()))
+        elif mode == "span":
+            # tallies laid out back to back in one allocation (as backend.alloc_results places them): reduced in
+            # place as one range, with no packing copy (torch.cat must not be called)
+            blob = torch.zeros(1024 + 16 + 32, dtype=torch.uint8)
+            h = blob[:1024].view(torch.float32)
+            side = blob[1024:1032].view(torch.float32)
+            st = blob[1040:1060].view(torch.int32)
+            h.fill_(rank + 1.0)
+            side.fill_(2.0 * (rank + 1))
+            st.copy_(torch.arange(5, dtype=torch.int32) * (rank + 1))
+
+            def no_cat(*a, **k):
+                raise AssertionError("packing copy")
+            real, parallel.torch.cat = parallel.torch.cat, no_cat
+            try:
+                parallel.all_reduce_sums([h, side, st])
+            finally:
+                parallel.torch.cat = real
+            q.put((rank, h.tolist()[:2] + side.tolist(), 0, st.tolist()))
         elif mode == "exact":
             from oracle import oracle as orc
             d = np.load(os.path.join(GOLD, "exact_sum.npz"))
@@ -108,6 +127,13 @@ def test_all_reduce_sums_two_ranks():
     assert codes == [0, 0] and len(res) == 2
     for _, h, c, st in res:
         assert h == [3.0, 3.0] and c == 21 and st == [0, 3, 6, 9, 12]
+
+
+def test_all_reduce_in_place_over_adjacent_tallies():
+    res, codes = run2("span")
+    assert codes == [0, 0] and len(res) == 2
+    for _, h, _, st in res:
+        assert h == [3.0, 3.0, 6.0, 6.0] and st == [0, 3, 6, 9, 12]
 
 
 def test_exact_words_combine_two_ranks():
