@@ -52,6 +52,8 @@ TRAFFIC = {
     "rw_grad": ((5.241173e9 + 6.034955e9) / 1048576, 1048576),
     "rw_fwd": ((53075712 + 3524096) / 4194304, 4194304),
     "ph_fwd": ((10.557440e6 + 0.0) / 1048576, 1048576),
+    "od_grad": ((2.976084e9 + 3.093681e9) / 262144, 262144),
+    "od_fwd": ((0.009466e9 + 0.0) / 262144, 262144),
 }
 
 
@@ -580,6 +582,17 @@ def main():
     if cfg.name == "od":
         roofline = od_roofline(_lib, stream, dev, steps_total, replay_micro_steps(kk, C_used), f_ms, g_ms,
                                cfg.grad.kernel, cfg.fwd.kernel)
+        tr = TRAFFIC.get(cfg.grad.kernel)
+        if tr is not None:
+            # the replay's head buffer: every trial step's state written in the count pass and read in the sweep
+            mp = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+            hbm = json.load(open(mp)).get("hbm_gbs") if os.path.exists(mp) else None
+            roofline["traffic"] = int(round(tr[0] * N))
+            roofline["traffic_source"] = f"ncu dram bytes read+write of one launch at N={tr[1]}, scaled by items to N={N}"
+            gbs = roofline["traffic"] / (g_ms / 1e3) / 1e9
+            roofline["hbm"] = {"achieved": round(gbs, 2), "unit": "GB/s", "peak": hbm,
+                               "frac": round(gbs / hbm, 4) if hbm else None,
+                               "peak_source": "measured: MEASURED_PEAKS.json hbm_gbs" if hbm else None}
     if roofline is not None and not tree and cfg.name != "od":
         # per mode (the separate launches): the forward and the replay gradient against the same probe
         roofline["modes"] = {

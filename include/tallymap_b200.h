@@ -74,6 +74,14 @@ int tm_compile(const char* source, const char* include_dir, int32_t block, int32
  * Replaces: tallymap_kernel_info (backends/kernel/shim.cc:147-155). */
 int tm_kernel_info(int64_t id, long long* out);
 
+/* 1 when this build carries the XLA FFI handler `TallymapB200Launch` (tallymap_b200/csrc/tm_ffi.cc, compiled where
+ * XLA's FFI headers were on the include path), 0 otherwise.  The handler is the custom-call target a JAX install
+ * registers (jax.ffi.register_ffi_target(..., jax.ffi.pycapsule(lib.TallymapB200Launch), platform="CUDA")) with the
+ * reference's attributes kernel_id (int64), block (int32, checked against the kernel's registered block), n_zero
+ * (int32), flags (int32) and n_items (int64), and calls tm_launch on XLA's stream.
+ * Replaces: the XLA FFI handler symbol TallymapLaunch (backends/kernel/shim.cc:241-250). */
+int tm_ffi_available(void);
+
 /* Launch kernel `id` on `stream` (a cudaStream_t; NULL = the legacy default stream) over n_items items.
  *   bufs[n_args + n_rets]: device pointers, inputs then results; ret_bytes[n_rets]: each result's size in bytes
  *   n_zero: the first n_zero results are zeroed (cudaMemsetAsync on `stream`) before the launch

@@ -181,6 +181,15 @@ def _eval(e, a):
         return F32(v) if e.outs[0].dtype == T.F32 else int(v)
     if p == "convert":
         return _convert(a[0], d, e.outs[0].dtype)
+    if p == "bitcast":
+        src, dst = d, e.outs[0].dtype
+        if src == T.F32:
+            u = int(np.float32(a[0]).view(np.uint32))
+        else:
+            u = int(a[0]) & 0xFFFFFFFF
+        if dst == T.F32:
+            return np.uint32(u).view(np.float32)
+        return _wrap32(u) if dst == T.I32 else u
     if p == "threefry":
         return _tf(*a)
     if p == "bits":

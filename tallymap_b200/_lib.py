@@ -7,6 +7,7 @@ on a machine without a GPU).
 import ctypes
 import os
 import subprocess
+import sys
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -32,7 +33,7 @@ class TallymapError(RuntimeError):
 
 
 def sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h"))) + [
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h", ".cc"))) + [
         os.path.join(INCLUDE, "tallymap_b200.h")]
 
 
@@ -41,6 +42,17 @@ def nvcc():
         if c and (os.path.sep not in c or os.path.exists(c)):
             return c
     return "nvcc"
+
+
+def xla_ffi_include():
+    """-I flags for XLA's FFI headers when JAX is importable (jax.ffi.include_dir()), else none: the XLA FFI handler
+    (csrc/tm_ffi.cc) is then left out of the build and tm_ffi_available() returns 0"""
+    d = os.environ.get("TM_XLA_FFI_INCLUDE")
+    if not d:
+        r = subprocess.run([sys.executable, "-c", "import jax; print(jax.ffi.include_dir())"], capture_output=True,
+                           text=True)
+        d = r.stdout.strip() if r.returncode == 0 else ""
+    return ["-I", d] if d and os.path.isdir(d) else []
 
 
 def stale():
@@ -57,8 +69,8 @@ def build(force=False, verbose=False):
             return LIB
         os.makedirs(LIBDIR, exist_ok=True)
         tmp = LIB + ".tmp"
-        cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + [
-            "-o", tmp, os.path.join(CSRC, "tm_capi.cu")]
+        cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + xla_ffi_include() + [
+            "-o", tmp, os.path.join(CSRC, "tm_capi.cu"), os.path.join(CSRC, "tm_ffi.cc")]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise TallymapError("nvcc failed building libtm_b200.so:\n" + r.stdout + r.stderr)
@@ -93,6 +105,7 @@ def lib():
         L.tm_exact_scatter_noalloc.argtypes = [P, P, P, i64, i32, P, P]
         L.tm_math_eval.argtypes = [P, i32, P, P, P, i64]
         L.tm_probe_threefry.argtypes = [P, i32, P, i64, ctypes.POINTER(i64)]
+        L.tm_ffi_available.restype = ctypes.c_int
         L.tm_probe_issue.argtypes = [P, i32, i32, P, i64, ctypes.POINTER(i64)]
         L.tm_tree_generations.argtypes = [P, P, i64, i32, i32, i32, i32, P, P, P]
         L.tm_compile_register.argtypes = [i64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]
@@ -110,7 +123,7 @@ def check(rc):
 # the symbols include/tallymap_b200.h declares (tests check the library exports each one)
 EXPORTS = ("tm_abi_version", "tm_last_error", "tm_kernel_id", "tm_kernel_name", "tm_register", "tm_kernel_info",
            "tm_launch", "tm_check_status", "tm_exact_combine", "tm_exact_scatter", "tm_exact_scatter_noalloc",
-           "tm_probe_threefry", "tm_probe_issue", "tm_math_eval", "tm_tree_generations",
+           "tm_probe_threefry", "tm_probe_issue", "tm_ffi_available", "tm_math_eval", "tm_tree_generations",
            "tm_compile_register", "tm_compile")
 
 

@@ -1,0 +1,624 @@
+"""The jaxpr front end of the lowering: an item program as JAX traces it -- the closed jaxpr of ONE item that the
+reference builds in tallymap.vmap (tallymap/_api.py:559-668, ItemProgram.cj: invars = [tallies] + [per-item
+leaves] + [broadcast leaves], outvars = [tallies] + [per-item results]) -- turned into this package's scalar IR
+(trace.py), which lower.py compiles for sm_100a.  The reference lowers the same jaxprs with its own emitter
+(tallymap/backends/kernel/codegen.py:815, Emitter.run_jaxpr, over the op table of op_table.py).
+
+How: `item_function` returns a Python item function fn(t, *leaves) that INTERPRETS the jaxpr equation by
+equation with this package's traced values (lang / trace), so tracing it (trace.trace_item, or tallymap_b200.vmap
+of it) records exactly the IR a hand-written item of the same program would.  Each equation is read through
+`eqn.primitive.name`, `eqn.params`, `eqn.invars` / `eqn.outvars` and each variable's `aval` (shape, dtype); a
+literal operand has `.val`; sub-jaxprs (`while`'s cond_jaxpr / body_jaxpr, `cond`'s branches, `pjit`'s jaxpr) are
+interpreted in place.  Nothing here imports JAX: any objects with those attributes work (the CPU tests use
+duck-typed equation lists).
+
+Values: a scalar of shape () is a traced scalar or a numpy constant (equations whose operands are all constants are
+folded in numpy with the aval's dtype, as XLA would fold them); a small 1-D array is a trace.Vec; a PRNG key
+(typed key<fry>, or uint32[2] key data under random_wrap) is a trace.Key; a tally array is a reference to its
+output.  `tallymap_emit(t, idx, val)` becomes an emit at the flat index the reference's Tally.add has formed
+(out-of-range indices dropped and counted, _tally.py:29-57); `tallymap_spawn(q, when, *leaves)` a spawn.
+
+The primitives read are those of jax.numpy / jax.random / lax on scalars and small vectors that the reference's
+op table lowers (op_table.py:47 RULES): arithmetic, comparisons, bitwise and shifts, select_n, clamp, conversions
+and bitcasts, the transcendentals, integer_pow, the random primitives (random_seed / wrap / unwrap / fold_in /
+bits / split, threefry2x32), while (the item's one top-level loop), cond, pjit and the call wrappers, shape
+operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
+concatenate, iota, reductions).  Anything else raises UnsupportedError, as the reference's emitter does for a
+primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
+
+`run(p, pi, bc, target, cuda_math, schedule, ndev, min_blocks_per_sm)` is the reference's backend entry
+(tallymap/backends/kernel/__init__.py:135-185) over a reference ItemProgram: its jaxpr through this front end,
+compiled and launched through the C ABI, the outputs in the reference's order [sum tallies] + [stats] + [per-item
+results].
+"""
+import numpy as np
+
+from . import lang as tl
+from . import trace as T
+
+_DT = {"float32": T.F32, "int32": T.I32, "uint32": T.U32, "bool": T.BOOL}
+_NP = {T.F32: np.float32, T.I32: np.int32, T.U32: np.uint32, T.BOOL: np.bool_}
+
+
+def _is_key(aval):
+    return "key" in str(aval.dtype)
+
+
+def aval_spec(aval):
+    """the trace_item input spec of a jaxpr input: "f32" / "i32" / "u32" / "key" for a scalar, (dtype, n) for a
+    small vector"""
+    shape = tuple(aval.shape)
+    if _is_key(aval):
+        if shape != ():
+            raise T.UnsupportedError("tallymap_b200.from_jaxpr: a per-item key operand must be one key")
+        return "key"
+    dt = _DT.get(str(aval.dtype))
+    if dt is None or dt == T.BOOL:
+        raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: operand dtype {aval.dtype} is not lowered")
+    if shape == ():
+        return dt
+    if len(shape) == 1:
+        return (dt, int(shape[0]))
+    raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: operand shape {shape} is not lowered")
+
+
+class _TallyRef(T.TallyToken):
+    """a tally array of the jaxpr (one Sum output, or the spawn queue token): the item's tally handle, and which
+    output it is; the loop carries it as the tracer carries the handle"""
+
+    def __init__(self, tok, name):          # (the handle's state stays on `tok`)
+        self.tok, self.name = tok, name
+
+
+def _dtype(aval):
+    return _DT.get(str(aval.dtype))
+
+
+def _const(val, aval):
+    """a literal operand -> a numpy scalar of its dtype, or a Vec of them"""
+    dt = _dtype(aval)
+    if dt is None:
+        raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: literal of dtype {aval.dtype}")
+    a = np.asarray(val, dtype=_NP[dt])
+    if a.shape == ():
+        return _NP[dt](a)
+    return T.Vec(_NP[dt](x) for x in a.reshape(-1))
+
+
+def _isconst(x):
+    return isinstance(x, np.generic) or (isinstance(x, T.Vec) and all(isinstance(v, np.generic) for v in x))
+
+
+def _py(x):
+    """numpy constants -> Python numbers (the tracer's literals take the traced operand's type)"""
+    if isinstance(x, np.generic):
+        return x.item()
+    if isinstance(x, T.Vec):
+        return T.Vec(_py(v) for v in x)
+    return x
+
+
+def _cast(x, dt):
+    """a traced or constant value as dtype dt (numpy for constants, astype for traced values)"""
+    if isinstance(x, T.Vec):
+        return T.Vec(_cast(v, dt) for v in x)
+    if isinstance(x, np.generic):
+        if dt == T.I32 or dt == T.U32:
+            if isinstance(x, np.floating):
+                with np.errstate(all="ignore"):
+                    f = np.float32(x)
+                    if np.isnan(f):
+                        return _NP[dt](0)
+                    lo, hi = (-2 ** 31, 2 ** 31 - 1) if dt == T.I32 else (0, 2 ** 32 - 1)
+                    return _NP[dt](int(np.clip(np.trunc(np.float64(f)), lo, hi)))
+            return _NP[dt](int(x) & 0xFFFFFFFF if dt == T.U32 else ((int(x) + 2 ** 31) % 2 ** 32) - 2 ** 31)
+        if dt == T.BOOL:
+            return np.bool_(x != 0)
+        return np.float32(x)
+    x = T._lit(x)
+    return x.astype(dt) if x.dtype != dt else x
+
+
+# ------------------------------------------------------------------------------------------------ elementwise
+def _fold(fn, args, dt):
+    """fn over numpy constants in dtype dt (elementwise over Vecs)"""
+    if any(isinstance(a, T.Vec) for a in args):
+        n = max(len(a) for a in args if isinstance(a, T.Vec))
+        at = lambda a, i: tuple.__getitem__(a, i) if isinstance(a, T.Vec) else a
+        return T.Vec(_fold(fn, [at(a, i) for a in args], dt) for i in range(n))
+    with np.errstate(all="ignore"):
+        r = fn(*args)
+    return _NP[dt](r) if dt is not None else r
+
+
+def _np_trunc_div(a, b):
+    if b == 0:
+        return -1
+    q = abs(int(a)) // abs(int(b))
+    return q if (a < 0) == (b < 0) else -q
+
+
+def _np_trunc_rem(a, b):
+    if b == 0:
+        return int(a)
+    return int(a) - _np_trunc_div(a, b) * int(b)
+
+
+_FOLD2 = {
+    "add": lambda a, b: a + b, "sub": lambda a, b: a - b, "mul": lambda a, b: a * b,
+    "max": lambda a, b: np.maximum(a, b) if not (np.isnan(a) or np.isnan(b)) else a + b,
+    "min": lambda a, b: np.minimum(a, b) if not (np.isnan(a) or np.isnan(b)) else a + b,
+    "eq": lambda a, b: a == b, "ne": lambda a, b: a != b, "lt": lambda a, b: a < b, "le": lambda a, b: a <= b,
+    "gt": lambda a, b: a > b, "ge": lambda a, b: a >= b,
+    "and": lambda a, b: a & b, "or": lambda a, b: a | b, "xor": lambda a, b: a ^ b,
+}
+
+
+def _tdiv(a, b, dt):
+    """lax.div: float division, or integer division truncated toward zero (lax semantics)"""
+    if dt == T.F32:
+        return a / b
+    if dt == T.U32:
+        return a // b
+    q = a // b                                        # floor division
+    fix = ((a % b) != 0) & ((a < 0) != (b < 0))
+    return q + fix.astype(tl.int32)
+
+
+def _trem(a, b, dt):
+    """lax.rem: C's remainder (the sign of the dividend)"""
+    if dt == T.F32:
+        return tl.rem(a, b)
+    if dt == T.U32:
+        return a % b
+    r = a % b                                         # floor modulo
+    return tl.where((r != 0) & ((a < 0) != (b < 0)), r - b, r)
+
+
+def _shift_right_logical(a, b, dt):
+    if dt == T.U32:
+        return a >> b
+    return tl.bitcast_convert_type(tl.bitcast_convert_type(a, tl.uint32) >> _cast(b, T.U32), tl.int32)
+
+
+def _shift_right_arithmetic(a, b, dt):
+    if dt == T.I32:
+        return a >> b
+    return tl.bitcast_convert_type(tl.bitcast_convert_type(a, tl.int32) >> _cast(b, T.I32), tl.uint32)
+
+
+def _round(x, method):
+    """lax.round: rounding_method 1 (ROUND_TO_NEAREST_EVEN, jnp.round) or 0 (AWAY_FROM_ZERO)"""
+    if int(method) == 1:
+        return tl.round(x)
+    t = tl.sign(x) * tl.floor(tl.abs(x))              # toward zero
+    return tl.where(tl.abs(x - t) >= 0.5, t + tl.sign(x), t)
+
+
+_UNARY = {
+    "exp": tl.exp, "log": tl.log, "sin": tl.sin, "cos": tl.cos, "tan": tl.tan, "tanh": tl.tanh, "sqrt": tl.sqrt,
+    "log1p": tl.log1p, "expm1": tl.expm1, "atan": tl.arctan, "asin": tl.arcsin, "acos": tl.arccos,
+    "sinh": tl.sinh, "cosh": tl.cosh, "asinh": tl.arcsinh, "acosh": tl.arccosh, "atanh": tl.arctanh,
+    "erf": tl.erf, "erfc": tl.erfc, "erf_inv": tl.erfinv, "exp2": tl.exp2, "cbrt": tl.cbrt, "logistic": tl.logistic,
+    "floor": tl.floor, "ceil": tl.ceil, "abs": tl.abs, "sign": tl.sign, "is_finite": tl.isfinite,
+    "stop_gradient": tl.stop_gradient, "square": lambda x: x * x, "neg": lambda x: -x, "not": lambda x: ~x,
+    "rsqrt": lambda x: 1.0 / tl.sqrt(x),
+}
+_NP_UNARY = {"neg": np.negative, "abs": np.abs, "not": np.invert, "floor": np.floor, "ceil": np.ceil,
+             "sign": np.sign, "exp": np.exp, "log": np.log, "sqrt": np.sqrt, "square": np.square}
+
+
+class UnsupportedPrimitive(T.UnsupportedError):
+    pass
+
+
+class _Interp:
+    """evaluates jaxprs over traced values; `tok` is the item's tally handle, `names` the tally outputs in invar
+    order (the spawn queue as '__spawn__')"""
+
+    def __init__(self, tok):
+        self.tok = tok
+        self.depth = 0            # > 0 inside the top-level loop's cond / body
+
+    # -------------------------------------------------------------------------------------------- plumbing
+    def read(self, env, v):
+        if hasattr(v, "val"):
+            return _const(v.val, v.aval)
+        return env[id(v)]
+
+    def eval(self, jaxpr, consts, args):
+        env = {}
+        for v, c in zip(getattr(jaxpr, "constvars", ()), consts):
+            env[id(v)] = _const(c, v.aval) if not isinstance(c, (T.Var, T.Vec, T.Key)) else c
+        if len(args) != len(jaxpr.invars):
+            raise T.TraceError(f"tallymap_b200.from_jaxpr: {len(args)} values for {len(jaxpr.invars)} inputs")
+        for v, a in zip(jaxpr.invars, args):
+            env[id(v)] = a
+        for e in jaxpr.eqns:
+            ins = [self.read(env, v) for v in e.invars]
+            outs = self.apply(e, ins)
+            for v, o in zip(e.outvars, outs):
+                env[id(v)] = o
+        return [self.read(env, v) for v in jaxpr.outvars]
+
+    def call(self, closed, args):
+        jaxpr = getattr(closed, "jaxpr", closed)
+        consts = getattr(closed, "consts", ())
+        return self.eval(jaxpr, list(consts), list(args))
+
+    # -------------------------------------------------------------------------------------------- equations
+    def apply(self, e, a):
+        p = e.primitive.name
+        prm = e.params
+        out_aval = e.outvars[0].aval if e.outvars else None
+        odt = _dtype(out_aval) if out_aval is not None else None
+        idt = _dtype(e.invars[0].aval) if e.invars and not _is_key(e.invars[0].aval) else None
+
+        # calls: interpreted in place
+        if p in ("pjit", "closed_call", "core_call", "remat", "checkpoint", "custom_jvp_call", "custom_vjp_call",
+                 "custom_vjp_call_jaxpr", "custom_lin"):
+            sub = prm.get("jaxpr") or prm.get("call_jaxpr") or prm.get("fun_jaxpr")
+            if sub is None:
+                raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} without a jaxpr")
+            n = len(getattr(sub, "jaxpr", sub).invars)
+            return self.call(sub, a[:n])
+        if p == "while":
+            return self.while_(e, a)
+        if p == "cond":
+            return self.cond(e, a)
+        if p == "tallymap_emit":
+            ref, idx, val = a
+            if not isinstance(ref, _TallyRef):
+                raise T.TraceError("tallymap_b200.from_jaxpr: an emit into something other than a tally")
+            idxs = list(idx) if isinstance(idx, T.Vec) else [idx]
+            vals = list(val) if isinstance(val, T.Vec) else [val] * len(idxs)
+            for i, v in zip(idxs, vals):
+                T._add_flat(self.tok, ref.name, _py(i), _py(v))
+            return [ref]
+        if p == "tallymap_spawn":
+            q, when, *leaves = a
+            self.tok.spawn(tuple(_py(x) for x in leaves), when=_py(when))
+            return [q]
+        if p in _RANDOM:
+            return _RANDOM[p](self, e, a)
+        if p == "threefry2x32":
+            k0, k1, x0, x1 = [_py(x) for x in a]
+            o = T._cur().emit("threefry", [T._lit(_cast(k0, T.U32)), T._lit(_cast(k1, T.U32)),
+                                           T._lit(_cast(x0, T.U32)), T._lit(_cast(x1, T.U32))], [T.U32, T.U32])
+            return list(o)
+
+        # shape operations on scalars and small vectors
+        if p in ("reshape", "squeeze", "expand_dims", "copy", "copy_p", "optimization_barrier", "broadcast_in_dim",
+                 "convert_element_type", "bitcast_convert_type", "reduce_precision"):
+            return [self.shape_op(p, e, a, odt)]
+        if p == "iota":
+            n = int(prm["shape"][0]) if prm.get("shape") else 1
+            return [T.Vec(_NP[odt](i) for i in range(n))]
+        if p == "slice":
+            (x,) = a
+            s0, s1 = int(prm["start_indices"][0]), int(prm["limit_indices"][0])
+            st = int(prm["strides"][0]) if prm.get("strides") else 1
+            return [T.Vec(tuple.__getitem__(x, i) for i in range(s0, s1, st))]
+        if p == "dynamic_slice":
+            x, i = a[0], a[1]
+            size = int(prm["slice_sizes"][0])
+            n = len(x)
+            if isinstance(i, np.generic):
+                s = int(np.clip(int(i), 0, n - size))
+                return [T.Vec(tuple.__getitem__(x, j) for j in range(s, s + size))]
+            if size != 1:
+                raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: dynamic_slice of more than one element at a "
+                                           "traced index")
+            return [T.Vec([_index_clamped(x, _py(i))])]
+        if p == "concatenate":
+            out = []
+            for x in a:
+                out += list(x) if isinstance(x, T.Vec) else [x]
+            return [T.Vec(out)]
+        if p in ("reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "argmax", "argmin"):
+            (x,) = a
+            if _isconst(x):
+                f = {"reduce_sum": np.sum, "reduce_max": np.max, "reduce_min": np.min, "reduce_and": np.all,
+                     "reduce_or": np.any, "argmax": np.argmax, "argmin": np.argmin}[p]
+                return [_NP[odt](f(np.array(list(x))))]
+            f = {"reduce_sum": tl.sum, "reduce_max": tl.max, "reduce_min": tl.min, "reduce_and": tl.all,
+                 "reduce_or": tl.any, "argmax": tl.argmax, "argmin": tl.argmin}[p]
+            return [f(_py(x))]
+
+        # elementwise
+        if p == "select_n":
+            which, *cases = a
+            if _isconst(which) and not isinstance(which, T.Vec):
+                return [cases[int(which)]]
+            if len(cases) == 2:
+                c = _py(which)
+                if _dtype(e.invars[0].aval) != T.BOOL:
+                    c = c != 0
+                return [tl.where(c, _py(cases[1]), _py(cases[0]))]
+            r = _py(cases[0])
+            for j in range(1, len(cases)):
+                r = tl.where(_py(which) == j, _py(cases[j]), r)
+            return [r]
+        if p == "clamp":
+            lo, x, hi = a
+            if all(_isconst(v) for v in a):
+                return [_fold(lambda l, x_, h: np.minimum(np.maximum(x_, l), h), [lo, x, hi], odt)]
+            return [tl.minimum(tl.maximum(_py(x), _py(lo)), _py(hi))]
+        if p == "integer_pow":
+            (x,) = a
+            y = int(prm["y"])
+            if _isconst(x):
+                return [_fold(lambda v: v ** y if y >= 0 else 1 / v ** -y, [x], odt)]
+            return [_vec(lambda v: T.int_pow(v, y), _py(x))]
+        if p == "round":
+            (x,) = a
+            return [_vec(lambda v: _round(v, prm.get("rounding_method", 0)), _py(x))]
+        if p in _UNARY:
+            (x,) = a
+            if _isconst(x) and p in _NP_UNARY:
+                return [_fold(_NP_UNARY[p], [x], odt)]
+            if _isconst(x):
+                raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of a constant is not folded")
+            return [_UNARY[p](_py(x))]
+        if p in ("div", "rem", "pow", "atan2", "nextafter", "shift_left", "shift_right_logical",
+                 "shift_right_arithmetic") or p in _FOLD2:
+            x, y = a
+            if _isconst(x) and _isconst(y):
+                return [self.fold2(p, x, y, idt, odt)]
+            x, y = _py(x), _py(y)
+            if p == "div":
+                return [_tdiv(x, y, idt)]
+            if p == "rem":
+                return [_trem(x, y, idt)]
+            if p == "pow":
+                return [tl.power(x, y)]
+            if p == "atan2":
+                return [tl.arctan2(x, y)]
+            if p == "nextafter":
+                return [tl.nextafter(x, y)]
+            if p == "shift_left":
+                return [x << y]
+            if p == "shift_right_logical":
+                return [_shift_right_logical(x, y, idt)]
+            if p == "shift_right_arithmetic":
+                return [_shift_right_arithmetic(x, y, idt)]
+            ops = {"add": lambda: x + y, "sub": lambda: x - y, "mul": lambda: x * y,
+                   "max": lambda: tl.maximum(x, y), "min": lambda: tl.minimum(x, y),
+                   "eq": lambda: x == y, "ne": lambda: x != y, "lt": lambda: x < y, "le": lambda: x <= y,
+                   "gt": lambda: x > y, "ge": lambda: x >= y, "and": lambda: x & y, "or": lambda: x | y,
+                   "xor": lambda: x ^ y}
+            if not isinstance(x, (T.Var, T.Vec)):       # (a constant on the left: the traced operand's method)
+                if p in ("add", "mul", "and", "or", "xor", "eq", "ne", "max", "min"):
+                    x, y = y, x
+                    ops = {**ops, **{k: v for k, v in ops.items()}}
+                    return [{"add": lambda: x + y, "mul": lambda: x * y, "and": lambda: x & y,
+                             "or": lambda: x | y, "xor": lambda: x ^ y, "eq": lambda: x == y,
+                             "ne": lambda: x != y, "max": lambda: tl.maximum(y, x),
+                             "min": lambda: tl.minimum(y, x)}[p]()]
+                flip = {"lt": "gt", "le": "ge", "gt": "lt", "ge": "le"}
+                if p in flip:
+                    x, y = y, x
+                    return [ops[flip[p]]()]
+            return [ops[p]()]
+        raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: primitive {p!r} is not lowered")
+
+    def fold2(self, p, x, y, idt, odt):
+        if p == "div":
+            return _fold(lambda a, b: a / b if idt == T.F32 else _np_trunc_div(a, b), [x, y], odt)
+        if p == "rem":
+            return _fold(lambda a, b: np.fmod(a, b) if idt == T.F32 else _np_trunc_rem(a, b), [x, y], odt)
+        if p == "pow":
+            return _fold(lambda a, b: np.float32(np.float64(a) ** np.float64(b)), [x, y], odt)
+        if p == "shift_left":
+            return _fold(lambda a, b: 0 if int(b) >= 32 else (int(a) << int(b)) & 0xFFFFFFFF, [x, y], None) \
+                if odt == T.U32 else _fold(lambda a, b: _cast(np.uint32(0 if int(b) >= 32 else
+                                                                        (int(a) << int(b)) & 0xFFFFFFFF), T.I32),
+                                           [x, y], odt)
+        if p in ("shift_right_logical", "shift_right_arithmetic"):
+            raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of constants is not folded")
+        if p in _FOLD2:
+            return _fold(_FOLD2[p], [x, y], odt)
+        raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of constants is not folded")
+
+    def shape_op(self, p, e, a, odt):
+        x = a[0]
+        shape = tuple(e.outvars[0].aval.shape)
+        if p == "convert_element_type":
+            return _cast(x, _DT[str(e.params["new_dtype"])] if str(e.params["new_dtype"]) in _DT else odt)
+        if p == "bitcast_convert_type":
+            if _isconst(x):
+                return _fold(lambda v: np.array([v]).view(_NP[odt])[0], [x], odt)
+            return tl.bitcast_convert_type(_py(x), {T.F32: tl.float32, T.I32: tl.int32, T.U32: tl.uint32}[odt])
+        if p == "reduce_precision":
+            return x
+        n = int(np.prod(shape)) if shape else 1
+        if shape == () or n == 1 and len(shape) <= 1 and not isinstance(x, T.Vec):
+            if isinstance(x, T.Vec):
+                if len(x) != 1:
+                    raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of {len(x)} elements to a scalar")
+                x = tuple.__getitem__(x, 0)
+            return T.Vec([x]) if shape == (1,) else x
+        if len(shape) != 1:
+            raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: arrays of shape {shape} are not lowered")
+        if isinstance(x, T.Vec):
+            if len(x) == n:
+                return x
+            if len(x) == 1:
+                return T.Vec([tuple.__getitem__(x, 0)] * n)
+            raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} from {len(x)} to {n} elements")
+        return T.Vec([x] * n)
+
+    # -------------------------------------------------------------------------------------------- control flow
+    def while_(self, e, a):
+        prm = e.params
+        cn, bn = int(prm["cond_nconsts"]), int(prm["body_nconsts"])
+        cconst, bconst, init = a[:cn], a[cn:cn + bn], a[cn + bn:]
+        if self.depth > 0:
+            raise T.UnsupportedError("tallymap_b200.from_jaxpr: a while loop inside the item's loop (nested loops "
+                                     "are not lowered)")
+        self.depth += 1
+        try:
+            flat = [(_py(x) if not isinstance(x, T.Vec) else _py(x)) for x in init]
+
+            def cond_fun(c):
+                return _py(self.call(prm["cond_jaxpr"], list(cconst) + list(c))[0])
+
+            def body_fun(c):
+                return tuple(_py(x) for x in self.call(prm["body_jaxpr"], list(bconst) + list(c)))
+            out = tl.while_loop(cond_fun, body_fun, tuple(flat))
+        finally:
+            self.depth -= 1
+        return list(out)
+
+    def cond(self, e, a):
+        idx, *ops = a
+        branches = e.params["branches"]
+        fns = [(lambda br: (lambda *xs: tuple(_py(v) for v in self.call(br, list(xs)))))(br) for br in branches]
+        if _isconst(idx):
+            return list(fns[int(np.clip(int(idx), 0, len(fns) - 1))](*[_py(x) for x in ops]))
+        i = _py(idx)
+        if _dtype(e.invars[0].aval) == T.BOOL:
+            i = i.astype(tl.int32)
+        r = tl.switch(i, fns, *[_py(x) for x in ops])
+        return list(r) if isinstance(r, tuple) else [r]
+
+
+def _vec(f, x):
+    return T.Vec(f(v) for v in x) if isinstance(x, T.Vec) else f(x)
+
+
+def _index_clamped(x, i):
+    n = len(x)
+    i = tl.clip(i, 0, n - 1) if not isinstance(i, int) else int(np.clip(i, 0, n - 1))
+    return tuple.__getitem__(x, i) if isinstance(i, int) else x[i]
+
+
+# ------------------------------------------------------------------------------------------------ jax.random
+def _key_of(x):
+    if isinstance(x, T.Key):
+        return x
+    if isinstance(x, T.Vec) and len(x) == 2:
+        return T.Key(T._lit(_cast(tuple.__getitem__(x, 0), T.U32)), T._lit(_cast(tuple.__getitem__(x, 1), T.U32)))
+    raise T.TraceError("tallymap_b200.from_jaxpr: a PRNG key was expected")
+
+
+def _r_seed(it, e, a):
+    (s,) = a
+    s = _py(s)
+    seed = T.Lit(int(s) & 0xFFFFFFFF, T.U32) if isinstance(s, int) else _cast(s, T.U32)
+    return [T.Key(T.Lit(0, T.U32) if not isinstance(s, int) or s >= 0 else T.Lit(0xFFFFFFFF, T.U32), seed)]
+
+
+def _r_wrap(it, e, a):
+    return [_key_of(a[0])]
+
+
+def _r_unwrap(it, e, a):
+    k = _key_of(a[0])
+    return [T.Vec([k.a, k.b])]
+
+
+def _r_fold_in(it, e, a):
+    k, m = a
+    return [tl.random.fold_in(_key_of(k), _py(m))]
+
+
+def _r_bits(it, e, a):
+    if int(e.params.get("bit_width", 32)) != 32:
+        raise T.UnsupportedError("tallymap_b200.from_jaxpr: random_bits of a width other than 32")
+    shape = tuple(e.params.get("shape", ()))
+    if len(shape) > 1:
+        raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: random_bits of shape {shape}")
+    return [tl.random.bits(_key_of(a[0]), shape if shape else ())]
+
+
+def _r_split(it, e, a):
+    shape = tuple(e.params.get("shape", (2,)))
+    n = int(np.prod(shape))
+    return [_KeyVec(tl.random.split(_key_of(a[0]), n))]
+
+
+class _KeyVec(tuple):
+    """the keys of random_split (indexed by the slicing that follows it)"""
+
+
+_RANDOM = {"random_seed": _r_seed, "random_wrap": _r_wrap, "random_unwrap": _r_unwrap, "random_fold_in": _r_fold_in,
+           "random_bits": _r_bits, "random_split": _r_split}
+
+
+# ------------------------------------------------------------------------------------------------ the item
+def item_function(closed, tallies, n_per_item):
+    """-> (fn, in_specs): fn(t, *leaves) interprets the item jaxpr `closed` (invars [tallies] + [per-item leaves] +
+    [broadcast leaves], outvars [tallies] + [per-item results]); tallies: the names of its tally inputs in order
+    (a spawn queue token named '__spawn__'); in_specs: trace_item's spec of each leaf."""
+    jaxpr = getattr(closed, "jaxpr", closed)
+    nT = len(tallies)
+    specs = [aval_spec(v.aval) for v in jaxpr.invars[nT:]]
+
+    def fn(t, *leaves):
+        it = _Interp(t)
+        refs = [_TallyRef(t, name) for name in tallies]
+        vals = []
+        for x, s in zip(leaves, specs):
+            vals.append(x)
+        outs = it.call(closed, refs + vals)
+        for o, name in zip(outs[:nT], tallies):
+            if not (isinstance(o, _TallyRef) and o.name == name):
+                raise T.TallyError(f"tallymap_b200.from_jaxpr: tally output {name!r} is not the tally it received")
+        res = []
+        for o in outs[nT:]:
+            if isinstance(o, (T.Key, _KeyVec)):
+                raise T.UnsupportedError("tallymap_b200.from_jaxpr: a key as a per-item result")
+            if isinstance(o, np.bool_):
+                o = bool(o)
+            res.append(_py(o) if not isinstance(o, T.Vec) else _py(o))
+        return (t,) + tuple(res)
+    return fn, specs
+
+
+# ------------------------------------------------------------------------------------------------ backend entry
+_PROGRAMS = {}
+
+
+def run(p, pi, bc, target="cuda", cuda_math="approx", schedule="item", ndev=1, min_blocks_per_sm=None, **_):
+    """The reference's backend entry (tallymap/backends/kernel/__init__.py:135-185) over a reference ItemProgram
+    `p` (p.cj: the item's closed jaxpr after retrace(cap) -- its loop counter and `truncated` result included --;
+    p.tallies: TSpec-like entries with .name, .kind ('sum' / 'spawn'), .dtype, .size or .shape; p.nP / p.nB: the
+    per-item / broadcast leaf counts; p.spawn: a Queue-like with .capacity or None).  pi / bc: the per-item and
+    broadcast leaves (keys as uint32[..., 2] key data, as KB.run passes them).  -> [sum tallies] + [stats int32[5]]
+    + [per-item results], as torch tensors on the current CUDA device, in the reference's order.
+
+    The jaxpr's own loop counter enforces max_steps (retrace(cap)); the backend's runtime ceiling is set above it.
+    target must be 'cuda' (no CPU fallback); cuda_math / min_blocks_per_sm are the lowering's options (an unknown
+    cuda_math raises); schedule is accepted for signature compatibility (the runtime refills at step granularity
+    either way); ndev > 1 partitions are the caller's (each rank runs its own items, tallymap_b200.parallel)."""
+    if target != "cuda":
+        raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
+    from . import api
+    import torch
+    sums = [s for s in p.tallies if getattr(s, "kind", "sum") == "sum"]
+    names = [s.name for s in p.tallies]
+    key = (id(p.cj), cuda_math, min_blocks_per_sm)
+    mf = _PROGRAMS.get(key)
+    if mf is None:
+        fn, specs = item_function(p.cj, names, int(p.nP))
+        outputs = {}
+        for s in sums:
+            shape = tuple(getattr(s, "shape", None) or (int(s.size),))
+            dt = torch.int32 if "int" in str(s.dtype) else torch.float32
+            outputs[s.name] = api.Sum(shape, dt)
+        spawn = getattr(p, "spawn", None)
+        opts = {"cuda_math": "ieee" if cuda_math is None else cuda_math}
+        if min_blocks_per_sm is not None:
+            opts["min_blocks_per_sm"] = int(min_blocks_per_sm)
+        mf = api.vmap(fn, outputs=outputs, in_axes=(0,) * int(p.nP) + (None,) * int(p.nB), max_steps=2 ** 31 - 1,
+                      spawn=api.Queue(int(spawn.capacity)) if spawn is not None else None, **opts)
+        mf._jaxpr_specs = specs
+        _PROGRAMS[key] = mf
+    r = mf(*pi, *bc)
+    outs = [r.raw_outputs[s.name] if hasattr(r, "raw_outputs") else r.outputs[s.name] for s in sums]
+    stats = torch.stack([torch.as_tensor(r.stats[k]).reshape(()) for k in
+                         ("spawned", "children_dropped", "children_truncated", "fixed_point_overflow",
+                          "dropped_emits")]).to(torch.int32)
+    per = r.per_item if isinstance(r.per_item, (list, tuple)) else [r.per_item]
+    return outs + [stats] + list(per)

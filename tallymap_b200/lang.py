@@ -613,6 +613,25 @@ def interp(x, xp, fp, left=None, right=None):
     return where(x > xp[-1], fp[-1] if right is None else right, f)
 
 
+def bitcast_convert_type(x, new_dtype):
+    """lax.bitcast_convert_type between the 32-bit types (float32, int32, uint32): the same bits, another type"""
+    if isinstance(x, T.Vec):
+        return T.Vec(bitcast_convert_type(v, new_dtype) for v in x)
+    dst = T._dt(new_dtype)
+    x = T._lit(x)
+    if dst == T.BOOL or x.dtype == T.BOOL:
+        raise T.TraceError("tallymap_b200.lang.bitcast_convert_type: 32-bit types only")
+    if x.dtype == dst:
+        return x
+    if isinstance(x, T.Lit):
+        import numpy as np
+        src = {T.F32: np.float32, T.I32: np.int32, T.U32: np.uint32}[x.dtype]
+        out = {T.F32: np.float32, T.I32: np.int32, T.U32: np.uint32}[dst]
+        v = np.array([x.value], src).view(out)[0]
+        return T.Lit(float(v) if dst == T.F32 else int(v), dst)
+    return T._cur().emit("bitcast", [x], [dst])[0]
+
+
 def clip(x, a_min, a_max):
     """jnp.clip: maximum(a_min, x), then minimum(a_max, .) (lax.max / min semantics: NaN propagates)"""
     return minimum(a_max, maximum(a_min, x))

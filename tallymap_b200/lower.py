@@ -137,11 +137,23 @@ def c_expr(e, a):
         return f"__ldg(&{a[0]}[{a[1]}])"
     if p == "convert":
         return _convert(d, e.outs[0].dtype, a[0])
+    if p == "bitcast":  # lax.bitcast_convert_type between 32-bit types: the same bits
+        return _bitcast(d, e.outs[0].dtype, a[0])
     if p == "bits":
         return f"random_bits32(Key{{{a[0]}, {a[1]}}}, {a[2]})"
     if p == "uniform01":
         return f"uniform01(Key{{{a[0]}, {a[1]}}}, {a[2]})"
     raise LowerError(f"tallymap_b200.lower: no lowering for {p}")
+
+
+def _bitcast(src, dst, x):
+    if src == dst:
+        return f"({x})"
+    if src == T.F32:
+        return f"__float_as_uint({x})" if dst == T.U32 else f"__float_as_int({x})"
+    if dst == T.F32:
+        return f"__uint_as_float((u32)({x}))"
+    return f"({CTYPE[dst]})({x})"
 
 
 def _convert(src, dst, x):

@@ -484,6 +484,27 @@ class TallyToken:
         return self
 
 
+def _add_flat(tok, name, flat, value):
+    """tally[name].flat[flat] += value for a flat int32 index into the output's row-major layout (the index the
+    reference's Tally.add has already formed, with -1 for a coordinate out of range, _tally.py:260-271): the
+    emit of the jaxpr front end (tallymap_b200.from_jaxpr); out-of-range indices are dropped and counted"""
+    if name not in tok.specs:
+        raise TraceError(f"tallymap_b200: no output named {name!r} (outputs: {sorted(tok.specs)})")
+    _, dt = tok.specs[name]
+    i = _lit(flat)
+    if i.dtype == U32:
+        i = i.astype(I32) if isinstance(i, Var) else Lit(int(i.value), I32)
+    if i.dtype != I32:
+        raise TraceError("tallymap_b200: tally indices are int32")
+    v = _lit(value)
+    if isinstance(v, Lit):
+        v = Lit(float(v.value), F32) if dt == F32 else Lit(int(v.value), I32)
+    if v.dtype != dt:
+        raise TraceError(f"tallymap_b200: output {name!r} sums {dt}, got {v.dtype}")
+    _cur().eqns.append(Eqn("emit", [i, v], [], dict(tally=name)))
+    return tok
+
+
 def _flat_index(index, shape):
     """row-major flat index; any coordinate outside its dimension gives -1 (_tally.py:260-271)"""
     if not isinstance(index, tuple):
