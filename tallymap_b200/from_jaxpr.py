@@ -57,6 +57,8 @@ def aval_spec(aval):
         raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: operand dtype {aval.dtype} is not lowered")
     if shape == ():
         return dt
+    if dt == T.U32 and shape == (2,):
+        return "key"              # raw key data (jax.random.PRNGKey / split's uint32[2]): the two words of a key
     if len(shape) == 1:
         return (dt, int(shape[0]))
     raise T.UnsupportedError(f"tallymap_b200.from_jaxpr: operand shape {shape} is not lowered")
@@ -382,23 +384,12 @@ class _Interp:
                 return [_shift_right_logical(x, y, idt)]
             if p == "shift_right_arithmetic":
                 return [_shift_right_arithmetic(x, y, idt)]
+            # (a constant operand on either side: Python's reflected operators reach the traced operand's method)
             ops = {"add": lambda: x + y, "sub": lambda: x - y, "mul": lambda: x * y,
                    "max": lambda: tl.maximum(x, y), "min": lambda: tl.minimum(x, y),
                    "eq": lambda: x == y, "ne": lambda: x != y, "lt": lambda: x < y, "le": lambda: x <= y,
                    "gt": lambda: x > y, "ge": lambda: x >= y, "and": lambda: x & y, "or": lambda: x | y,
                    "xor": lambda: x ^ y}
-            if not isinstance(x, (T.Var, T.Vec)):       # (a constant on the left: the traced operand's method)
-                if p in ("add", "mul", "and", "or", "xor", "eq", "ne", "max", "min"):
-                    x, y = y, x
-                    ops = {**ops, **{k: v for k, v in ops.items()}}
-                    return [{"add": lambda: x + y, "mul": lambda: x * y, "and": lambda: x & y,
-                             "or": lambda: x | y, "xor": lambda: x ^ y, "eq": lambda: x == y,
-                             "ne": lambda: x != y, "max": lambda: tl.maximum(y, x),
-                             "min": lambda: tl.minimum(y, x)}[p]()]
-                flip = {"lt": "gt", "le": "ge", "gt": "lt", "ge": "le"}
-                if p in flip:
-                    x, y = y, x
-                    return [ops[flip[p]]()]
             return [ops[p]()]
         raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: primitive {p!r} is not lowered")
 
@@ -559,7 +550,9 @@ def item_function(closed, tallies, n_per_item):
         it = _Interp(t)
         refs = [_TallyRef(t, name) for name in tallies]
         vals = []
-        for x, s in zip(leaves, specs):
+        for x, v in zip(leaves, jaxpr.invars[nT:]):
+            if isinstance(x, T.Key) and not _is_key(v.aval):
+                x = T.Vec([x.a, x.b])            # raw uint32[2] key data, as the jaxpr reads it
             vals.append(x)
         outs = it.call(closed, refs + vals)
         for o, name in zip(outs[:nT], tallies):
@@ -595,30 +588,33 @@ def run(p, pi, bc, target="cuda", cuda_math="approx", schedule="item", ndev=1, m
     if target != "cuda":
         raise NotImplementedError("tallymap_b200 runs on CUDA devices only (no CPU fallback)")
     from . import api
+    from . import backend as B
     import torch
     sums = [s for s in p.tallies if getattr(s, "kind", "sum") == "sum"]
     names = [s.name for s in p.tallies]
     key = (id(p.cj), cuda_math, min_blocks_per_sm)
     mf = _PROGRAMS.get(key)
     if mf is None:
-        fn, specs = item_function(p.cj, names, int(p.nP))
+        fn, _ = item_function(p.cj, names, int(p.nP))
         outputs = {}
         for s in sums:
             shape = tuple(getattr(s, "shape", None) or (int(s.size),))
-            dt = torch.int32 if "int" in str(s.dtype) else torch.float32
-            outputs[s.name] = api.Sum(shape, dt)
+            outputs[s.name] = api.Sum(shape, torch.int32 if "int" in str(s.dtype) else torch.float32)
         spawn = getattr(p, "spawn", None)
         opts = {"cuda_math": "ieee" if cuda_math is None else cuda_math}
         if min_blocks_per_sm is not None:
             opts["min_blocks_per_sm"] = int(min_blocks_per_sm)
+        # the jaxpr's own loop counter caps the loop (retrace(cap)); the runtime's ceiling sits above it
         mf = api.vmap(fn, outputs=outputs, in_axes=(0,) * int(p.nP) + (None,) * int(p.nB), max_steps=2 ** 31 - 1,
                       spawn=api.Queue(int(spawn.capacity)) if spawn is not None else None, **opts)
-        mf._jaxpr_specs = specs
         _PROGRAMS[key] = mf
-    r = mf(*pi, *bc)
-    outs = [r.raw_outputs[s.name] if hasattr(r, "raw_outputs") else r.outputs[s.name] for s in sums]
-    stats = torch.stack([torch.as_tensor(r.stats[k]).reshape(()) for k in
-                         ("spawned", "children_dropped", "children_truncated", "fixed_point_overflow",
-                          "dropped_emits")]).to(torch.int32)
-    per = r.per_item if isinstance(r.per_item, (list, tuple)) else [r.per_item]
-    return outs + [stats] + list(per)
+    L = mf.lowered(tuple(pi) + tuple(bc))
+    spawn = getattr(p, "spawn", None)
+    out = B.run(L.fwd, list(pi), list(bc), consts=(mf.max_steps,),
+                queue=int(spawn.capacity) if spawn is not None else None)
+    nt = len(L.fwd.tallies)
+    stats = out[nt]
+    ys = out[nt + 1:][:L.n_results]
+    yav = [v.aval for v in getattr(p.cj, "jaxpr", p.cj).outvars[len(p.tallies):]]
+    per = [y.bool() if str(a.dtype) == "bool" else y for y, a in zip(ys, yav)]
+    return list(out[:nt]) + [stats] + per

@@ -190,6 +190,16 @@ class Var:
             raise TraceError("tallymap_b200.lang: % on integers only")
         return _binary("irem", self, o)
 
+    def __rfloordiv__(self, o):
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: // on integers only")
+        return _binary("idiv", o, self)
+
+    def __rmod__(self, o):
+        if self.dtype not in (I32, U32):
+            raise TraceError("tallymap_b200.lang: % on integers only")
+        return _binary("irem", o, self)
+
     def __neg__(self):
         return _cur().emit("neg", [self], [self.dtype])[0]
 
@@ -218,6 +228,12 @@ class Var:
         if self.dtype not in (I32, U32):
             raise TraceError("tallymap_b200.lang: >> on integers only")
         return _binary("shr", self, o)
+
+    def __rlshift__(self, o):
+        return _binary("shl", o, self)
+
+    def __rrshift__(self, o):
+        return _binary("shr", o, self)
 
     def __invert__(self):
         return _cur().emit("not", [self], [self.dtype])[0]

@@ -1,0 +1,157 @@
+"""Duck-typed jaxprs for the jaxpr front end's tests (JAX is not installed here): objects with the attributes
+tallymap_b200.from_jaxpr reads -- eqn.primitive.name / .params / .invars / .outvars, var.aval.shape / .dtype,
+literal.val, jaxpr.invars / .outvars / .eqns / .constvars, closed.jaxpr / .consts -- spelled the way jax.make_jaxpr
+writes the reference's quickstart item (examples/quickstart.py:19-30) under jax 0.6-0.8:
+
+    def walker(t, x, key, theta):
+        def body(c):
+            k, x, t = c
+            u = jax.random.uniform(jax.random.fold_in(key, k))
+            t = t.add("hist", (x * NB).astype(jnp.int32), theta * (1.0 - x))
+            return k + 1, x * (0.5 + 0.5 * u), t
+        k, x, t = lax.while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
+        return t, k
+
+with jax.random.split(PRNGKey(0), N)'s raw uint32[2] keys (fold_in and uniform wrap them with random_wrap and unwrap
+the result; uniform is a pjit of random_bits and the mantissa fill), the item's tally leaf first (ItemProgram.cj's
+invars: [tallies] + [per-item] + [broadcast]), and its retrace(cap=max_steps) form (the loop counter in the carry,
+`truncated` as a second per-item result: tallymap/_rewrite.py:251, 502-528)."""
+import itertools
+
+import numpy as np
+
+_ids = itertools.count()
+
+
+class Aval:
+    def __init__(self, shape, dtype):
+        self.shape, self.dtype = tuple(shape), dtype
+
+    def __repr__(self):
+        return f"{self.dtype}{list(self.shape)}"
+
+
+class Var:
+    def __init__(self, dtype, shape=()):
+        self.aval = Aval(shape, dtype)
+        self.n = next(_ids)
+
+
+class Literal:
+    def __init__(self, val, dtype):
+        self.val = val
+        self.aval = Aval((), dtype)
+
+
+class Primitive:
+    def __init__(self, name):
+        self.name = name
+
+
+class Eqn:
+    def __init__(self, prim, invars, outvars, **params):
+        self.primitive, self.invars, self.outvars, self.params = Primitive(prim), invars, outvars, params
+
+
+class Jaxpr:
+    def __init__(self, invars, outvars, eqns, constvars=()):
+        self.invars, self.outvars, self.eqns, self.constvars = invars, outvars, eqns, list(constvars)
+
+
+class ClosedJaxpr:
+    def __init__(self, jaxpr, consts=()):
+        self.jaxpr, self.consts = jaxpr, list(consts)
+
+
+F, I, U, B, KEY = "float32", "int32", "uint32", "bool", "key<fry>"
+
+
+def uniform_pjit():
+    """jax.random.uniform(key, (), f32, 0, 1) as the pjit jax.random.uniform binds: random_wrap, random_bits, the
+    mantissa fill, then max(lo, f * (hi - lo) + lo)"""
+    q, r, s = Var(U, (2,)), Var(F), Var(F)
+    t, u, v, w, x, y, z, ba, bb, bc, bd = (Var(KEY), Var(U), Var(U), Var(U), Var(F), Var(F), Var(F), Var(F), Var(F),
+                                           Var(F), Var(F))
+    eqns = [Eqn("random_wrap", [q], [t], impl="fry"),
+            Eqn("random_bits", [t], [u], bit_width=32, shape=()),
+            Eqn("shift_right_logical", [u, Literal(9, U)], [v]),
+            Eqn("or", [v, Literal(1065353216, U)], [w]),
+            Eqn("bitcast_convert_type", [w], [x], new_dtype="float32"),
+            Eqn("sub", [x, Literal(1.0, F)], [y]),
+            Eqn("sub", [s, r], [z]),
+            Eqn("mul", [y, z], [ba]),
+            Eqn("add", [ba, r], [bb]),
+            Eqn("reshape", [bb], [bc], new_sizes=(), dimensions=None),
+            Eqn("max", [r, bc], [bd])]
+    return ClosedJaxpr(Jaxpr([q, r, s], [bd], eqns))
+
+
+def quickstart(cap=None):
+    """the quickstart item's closed jaxpr; cap: retrace(cap=max_steps)'s form (loop counter + truncated result)"""
+    hist, x0, key, theta = Var(F, (16,)), Var(F), Var(U, (2,)), Var(F)
+    # body: consts (key, theta), carry ([cnt,] k, x, hist)
+    bkey, btheta = Var(U, (2,)), Var(F)
+    bcnt, bk, bx, bh = Var(I), Var(I), Var(F), Var(F, (16,))
+    m, ku, n, o, p = Var(KEY), Var(U), Var(KEY), Var(U, (2,)), Var(F)
+    be, bf, bg, bh2, bi, bj, bk2, bl, bm, bcnt2 = (Var(F), Var(I), Var(F), Var(F), Var(F, (16,)), Var(I), Var(F),
+                                                   Var(F), Var(F), Var(I))
+    body_eqns = [Eqn("random_wrap", [bkey], [m], impl="fry"),
+                 Eqn("convert_element_type", [bk], [ku], new_dtype="uint32", weak_type=False),
+                 Eqn("random_fold_in", [m, ku], [n]),
+                 Eqn("random_unwrap", [n], [o]),
+                 Eqn("pjit", [o, Literal(0.0, F), Literal(1.0, F)], [p], jaxpr=uniform_pjit(), name="_uniform"),
+                 Eqn("mul", [bx, Literal(16.0, F)], [be]),
+                 Eqn("convert_element_type", [be], [bf], new_dtype="int32", weak_type=False),
+                 Eqn("sub", [Literal(1.0, F), bx], [bg]),
+                 Eqn("mul", [btheta, bg], [bh2]),
+                 Eqn("tallymap_emit", [bh, bf, bh2], [bi]),
+                 Eqn("add", [bk, Literal(1, I)], [bj]),
+                 Eqn("mul", [Literal(0.5, F), p], [bk2]),
+                 Eqn("add", [Literal(0.5, F), bk2], [bl]),
+                 Eqn("mul", [bx, bl], [bm])]
+    carry_in = [bk, bx, bh]
+    carry_out = [bj, bm, bi]
+    if cap is not None:
+        body_eqns.append(Eqn("add", [bcnt, Literal(1, I)], [bcnt2]))
+        carry_in, carry_out = [bcnt] + carry_in, [bcnt2] + carry_out
+    body = ClosedJaxpr(Jaxpr([bkey, btheta] + carry_in, carry_out, body_eqns))
+    ccnt, ck, cx, ch, cq = Var(I), Var(I), Var(F), Var(F, (16,)), Var(B)
+    if cap is None:
+        cond = ClosedJaxpr(Jaxpr([ck, cx, ch], [cq], [Eqn("gt", [cx, Literal(0.05, F)], [cq])]))
+    else:
+        c1, c2 = Var(B), Var(B)
+        cond = ClosedJaxpr(Jaxpr([ccnt, ck, cx, ch], [cq], [Eqn("lt", [ccnt, Literal(cap, I)], [c1]),
+                                                             Eqn("gt", [cx, Literal(0.05, F)], [c2]),
+                                                             Eqn("and", [c1, c2], [cq])]))
+    ok, ox, oh, ocnt = Var(I), Var(F), Var(F, (16,)), Var(I)
+    outs = ([ocnt] if cap is not None else []) + [ok, ox, oh]
+    init = ([Literal(0, I)] if cap is not None else []) + [Literal(0, I), x0, hist]
+    eqns = [Eqn("while", [key, theta] + init, outs, cond_jaxpr=cond, body_jaxpr=body, cond_nconsts=0,
+                body_nconsts=2)]
+    results = [ok]
+    if cap is not None:                       # truncated = the loop ran out of steps with its predicate still true
+        t1, t2, tr = Var(B), Var(B), Var(B)
+        eqns += [Eqn("ge", [ocnt, Literal(cap, I)], [t1]), Eqn("gt", [ox, Literal(0.05, F)], [t2]),
+                 Eqn("and", [t1, t2], [tr])]
+        results.append(tr)
+    return ClosedJaxpr(Jaxpr([hist, x0, key, theta], [oh] + results, eqns))
+
+
+class TSpec:
+    """the reference's TSpec, as ItemProgram.tallies holds them (tallymap/_api.py:204-220)"""
+
+    def __init__(self, name, size, dtype="float32", kind="sum"):
+        self.name, self.size, self.dtype, self.kind = name, size, np.dtype(dtype), kind
+        self.shape = (size,)
+
+
+class ItemProgram:
+    """the fields of the reference's ItemProgram (tallymap/_api.py:231-281) the backend entry reads"""
+
+    def __init__(self, cj, tallies, nP, nB, trunc=None, spawn=None):
+        self.cj, self.tallies, self.nP, self.nB, self.trunc, self.spawn = cj, tuple(tallies), nP, nB, trunc, spawn
+        self.tag = "primal"
+
+
+def quickstart_program(cap=100):
+    return ItemProgram(quickstart(cap), [TSpec("hist", 16)], nP=2, nB=1, trunc=1)

@@ -1,0 +1,93 @@
+"""CPU: the jaxpr front end (tallymap_b200.from_jaxpr) on duck-typed jaxprs of the reference's quickstart item
+(tests/jaxpr_fixtures.py, spelled as jax.make_jaxpr writes it): the item function it makes traces to IR that the IR
+evaluator runs bitwise like the hand-written oracle (trip counts, truncation flags, stats; the histogram within the
+float tolerance) and like the same item written with tallymap_b200.lang; its retrace(cap) form gives the same
+trip counts and its own truncation flag; the lowering compiles it for sm_100a (NVRTC needs no GPU); primitives
+outside the table raise UnsupportedError."""
+import numpy as np
+import pytest
+
+import jaxpr_fixtures as J
+from tallymap_b200 import from_jaxpr as FJ
+from tallymap_b200 import prng
+from tallymap_b200 import trace as T
+
+SPECS = {"hist": ((16,), "f32")}
+
+
+def _inputs(n):
+    return np.linspace(0.1, 0.99, n, dtype=np.float32), prng.split(prng.PRNGKey(0), n)
+
+
+def test_quickstart_jaxpr_against_oracle(orc):
+    from oracle.ir_eval import Evaluator
+    fn, specs = FJ.item_function(J.quickstart(), ["hist"], 2)
+    assert specs == ["f32", "key", "f32"]
+    tr = T.trace_item(fn, specs, 2, SPECS)
+    assert sum(e.prim == "emit" for e in tr.body) == 1 and sum(e.prim == "bits" for e in tr.body) == 1
+    x, k = _inputs(3000)
+    r = Evaluator(tr, 100).run([x, k], [2.0])
+    ref = orc.q1_fwd(x, k, 2.0)
+    assert np.array_equal(r["results"][0], ref["k"]) and np.array_equal(r["trunc"], ref["trunc"])
+    assert np.array_equal(r["stats"], ref["stats"])
+    assert np.abs(r["sums"]["hist"] - ref["hist"]).max() <= 1e-6 * np.abs(ref["hist"]).max()
+    # the same item written with tallymap_b200.lang: the same results bitwise
+    from items_lang import quickstart
+    tq = T.trace_item(quickstart, ["f32", "key", "f32"], 2, SPECS)
+    rq = Evaluator(tq, 100).run([x, k], [2.0])
+    assert np.array_equal(rq["results"][0], r["results"][0])
+    assert np.array_equal(rq["sums"]["hist"].view(np.uint32), r["sums"]["hist"].view(np.uint32))
+
+
+def test_retraced_program_carries_its_own_cap(orc):
+    """the reference backend receives retrace(cap)'s program: its loop counter stops the loop and its own
+    `truncated` is the second per-item result, equal to the oracle's flags at max_steps = 3"""
+    from oracle.ir_eval import Evaluator
+    p = J.quickstart_program(cap=3)
+    fn, specs = FJ.item_function(p.cj, ["hist"], p.nP)
+    tr = T.trace_item(fn, specs, 2, SPECS)
+    x, k = _inputs(2000)
+    r = Evaluator(tr, 10 ** 6).run([x, k], [2.0])
+    ref = orc.q1_fwd(x, k, 2.0, max_steps=3)
+    assert ref["trunc"].any()
+    assert np.array_equal(r["results"][0], ref["k"])
+    assert np.array_equal(np.asarray(r["results"][1]).astype(bool), ref["trunc"])
+    assert not np.asarray(r["trunc"]).any()                # (the runtime's own ceiling is far above the cap)
+
+
+def test_lowers_and_compiles(tmlib):
+    import tallymap_b200 as tm
+    fn, specs = FJ.item_function(J.quickstart(), ["hist"], 2)
+    f = tm.vmap(fn, outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=100)
+    x, k = _inputs(8)
+    L = f.lowered((x, k, np.float32(2.0)))
+    assert isinstance(L.fwd.kernel, int) and "random_bits32" in L.fwd_source
+    g = L.grad_program((0,))          # the replay adjoint w.r.t. theta lowers from the same IR
+    assert g.tallies[0].exact
+
+
+def test_constant_folding_and_lax_integer_semantics():
+    """all-constant equations fold in numpy with the aval's dtype; lax.div / lax.rem of integers truncate toward
+    zero (not Python's floor), on traced values and on constants alike"""
+    from oracle.ir_eval import Evaluator
+    a, b, q, r, qc, rc, s = J.Var(J.I), J.Var(J.I), J.Var(J.I), J.Var(J.I), J.Var(J.I), J.Var(J.I), J.Var(J.F)
+    eqns = [J.Eqn("div", [a, b], [q]), J.Eqn("rem", [a, b], [r]),
+            J.Eqn("div", [J.Literal(-7, J.I), J.Literal(2, J.I)], [qc]),
+            J.Eqn("rem", [J.Literal(-7, J.I), J.Literal(2, J.I)], [rc]),
+            J.Eqn("sub", [J.Literal(1.0, J.F), J.Literal(0.25, J.F)], [s])]
+    cj = J.ClosedJaxpr(J.Jaxpr([a, b], [q, r, qc, rc, s], eqns))
+    fn, specs = FJ.item_function(cj, [], 2)
+    tr = T.trace_item(fn, specs, 2, {})
+    A = np.int32([7, -7, 7, -7, 0, 5])
+    Bv = np.int32([2, 2, -2, -2, 3, 5])
+    res = Evaluator(tr, 1).run([A, Bv], [])["results"]
+    assert list(res[0]) == [3, -3, -3, 3, 0, 1] and list(res[1]) == [1, -1, 1, -1, 0, 0]
+    assert list(res[2]) == [-3] * 6 and list(res[3]) == [-1] * 6 and np.all(np.asarray(res[4]) == 0.75)
+
+
+def test_unlowered_primitive_raises():
+    x, y = J.Var(J.F), J.Var(J.F)
+    cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
+    fn, specs = FJ.item_function(cj, [], 1)
+    with pytest.raises(T.UnsupportedError, match="'fft' is not lowered"):
+        T.trace_item(fn, specs, 1, {})

@@ -1,0 +1,43 @@
+"""GPU: the jaxpr front end end to end.  The reference's quickstart ItemProgram (duck-typed, tests/jaxpr_fixtures.py,
+after retrace(cap=100)) through tallymap_b200.from_jaxpr.run -- the reference backend entry's signature -- against
+the oracle: the histogram within the float tolerance, stats, trip counts and the program's own truncation flags
+bitwise, in the reference's output order [sum tallies] + [stats] + [per-item results]; and the same jaxpr's item
+function under tallymap_b200.vmap: its replay gradient w.r.t. theta bitwise the oracle's."""
+import numpy as np
+import pytest
+import torch
+
+import jaxpr_fixtures as J
+import tallymap_b200 as tm
+from tallymap_b200 import from_jaxpr as FJ
+from tallymap_b200 import prng
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(n):
+    return np.linspace(0.1, 0.99, n, dtype=np.float32), prng.split(prng.PRNGKey(0), n)
+
+
+@pytest.mark.parametrize("cap", [100, 3])
+def test_reference_item_program_runs(cuda, orc, cap):
+    x, k = _inputs(10000)
+    out = FJ.run(J.quickstart_program(cap=cap), [x, k], [np.float32(2.0)], target="cuda", cuda_math="ieee")
+    torch.cuda.synchronize()
+    hist, stats, kk, tr = [o.cpu().numpy() for o in out]
+    ref = orc.q1_fwd(x, k, 2.0, max_steps=cap)
+    assert out[3].dtype == torch.bool
+    assert np.array_equal(kk, ref["k"]) and np.array_equal(tr, ref["trunc"]) and np.array_equal(stats, ref["stats"])
+    assert np.abs(hist.astype(np.float64) - ref["hist"]).max() <= 1e-5 * np.abs(ref["hist"]).max()
+    if cap == 3:
+        assert tr.any()
+
+
+def test_jaxpr_item_gradient_bitwise(cuda, orc):
+    fn, _ = FJ.item_function(J.quickstart(), ["hist"], 2)
+    f = tm.vmap(fn, outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=100)
+    x, k = _inputs(10000)
+    ct = np.random.default_rng(5).normal(size=16).astype(np.float32)
+    g = f.grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.from_numpy(ct)})
+    ref = orc.q1_grad(x, k, 2.0, ct)
+    assert np.array_equal(np.float32(g.cpu().numpy()).reshape(1).view(np.uint32), ref["g"].view(np.uint32))
