@@ -207,11 +207,33 @@ struct RWFwd : RWCommon {
     return State{0, 0, __ldg(&c.x0[item])};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && pred(s.x); }
-  __device__ __forceinline__ static void step(const Ctx& c, State& s) {
-    const float u = uniform01(fold_in(c.key, (u32)s.kc));
+  // the step's uniform depends on the key and the step index only: draw(j) is step kc + j's, drawn ahead
+  // (tm_runtime.cuh, run_step), apply the step given its uniform; step = apply(draw(0))
+  static constexpr int kUnroll = 4;
+  typedef float Draw;
+  __device__ __forceinline__ static Draw draw(const Ctx& c, const State& s, int j) {
+    return uniform01(fold_in(c.key, (u32)(s.kc + j)));
+  }
+  __device__ __forceinline__ static void apply(const Ctx& c, State& s, Draw u) {
     SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.x * 256.0f), c.drift * s.x);
     s.kc += 1;
     s.x = move(s.x, u);
+  }
+  __device__ __forceinline__ static void step(const Ctx& c, State& s) { apply(c, s, draw(c, s, 0)); }
+  // an item in flight, movable to another thread of the block: its position, step count, key and index
+  struct Parked {
+    float x;
+    i32 kc;
+    u32 ka, kb;
+    i64 item;
+  };
+  __device__ __forceinline__ static Parked park(const Ctx& c, const State& s, i64 item) {
+    return Parked{s.x, s.kc, c.key.a, c.key.b, item};
+  }
+  __device__ __forceinline__ static State unpark(Ctx& c, const Parked& p, i64& item) {
+    c.key = Key{p.ka, p.kb};
+    item = p.item;
+    return State{p.kc, p.kc, p.x};
   }
   __device__ static void finish(const Ctx& c, const State& s, i64 item) {
     SumPriv<2>::emit(c.sh + kNB, c.stats, s.x > 1.0f ? 1 : 0, 1.0f);

@@ -82,15 +82,97 @@ __device__ __forceinline__ void finish_block(const typename I::Ctx& cx, u32* ctl
   }
 }
 
+// ------------------------------------------------------------------------------------------------ optional hooks
+// Two optional parts of the ITEM interface, detected at compile time:
+//
+// Draws (kUnroll > 1; typedef Draw; Draw draw(const Ctx&, const State&, int j); void apply(const Ctx&, State&,
+// const Draw&)): the random draws of the step kc + j depend only on the item's key and the step index, not on the
+// state (counter-based RNG: fold_in(key, kc) and its uniforms), so one iteration draws for up to kUnroll steps as
+// independent threefry chains and then applies the steps one after another while the loop predicate holds
+// (step == apply(draw(0))).  The chains interleave, so a warp that runs alone (the end of a launch, where a few long
+// items remain) is no longer bound by the latency of one dependent threefry chain.  The draws of the steps past the
+// item's end are wasted: at most kUnroll - 1 steps' draws per item.
+//
+// Parking (typedef Parked; Parked park(const Ctx&, const State&, i64 item); State unpark(Ctx&, const Parked&,
+// i64& item)): everything an item in flight needs besides the launch's context, so it can move to another thread of
+// the block.  Once the item counter runs dry, lanes whose items ended stay idle while their warp still steps the
+// others; with parking, the block instead gathers its items in flight every kEpoch iterations and deals them to its
+// first warps, so its stepping warps stay full and the others stop issuing.
+template <class T, class = void>
+struct draws_trait : tmstd::false_type {};
+template <class T>
+struct draws_trait<T, tmstd::void_t<decltype(T::kUnroll)>> : tmstd::integral_constant<bool, (T::kUnroll > 1)> {};
+template <class T, class = void>
+struct park_trait : tmstd::false_type {};
+template <class T>
+struct park_trait<T, tmstd::void_t<typename T::Parked>> : tmstd::true_type {};
+
+// one iteration's work for a lane whose loop predicate holds: one step, or up to kUnroll steps of pre-drawn
+// randomness (each after the first only while the predicate still holds)
+template <class I>
+__device__ __forceinline__ void run_step(const typename I::Ctx& cx, typename I::State& x) {
+  if constexpr (draws_trait<I>::value) {
+    typename I::Draw d[I::kUnroll];
+#pragma unroll
+    for (int j = 0; j < I::kUnroll; ++j) d[j] = I::draw(cx, x, j);
+    I::apply(cx, x, d[0]);
+#pragma unroll
+    for (int j = 1; j < I::kUnroll; ++j) {
+      if (!I::cond(cx, x)) break;
+      I::apply(cx, x, d[j]);
+    }
+  } else {
+    I::step(cx, x);
+  }
+}
+
+// The end of a launch for an ITEM with parking: every block runs its items in flight to their end in epochs of
+// kEpoch iterations, gathering them into a shared-memory pool before each epoch and dealing them to threads
+// 0, 1, ..., so the first ceil(L / 32) warps step full and the rest wait at the barrier (issuing nothing).
+// Items keep their per-item results and their emits (privatised tallies are the block's; a thread's private exact
+// words take whatever items it finishes), so moving an item changes no result.
+constexpr int kEpoch = 16;
+template <class I>
+__device__ __forceinline__ void forward_tail(typename I::Ctx& cx, typename I::State& x, i64& item, bool live) {
+  __shared__ typename I::Parked pool[TM_BLOCK];
+  __shared__ int pool_n;
+  for (;;) {
+    __syncthreads();                               // (the previous epoch's reads of the pool are done)
+    if (threadIdx.x == 0) pool_n = 0;
+    __syncthreads();
+    if (live) pool[atomicAdd(&pool_n, 1)] = I::park(cx, x, item);
+    __syncthreads();
+    const int n = pool_n;
+    if (n == 0) break;
+    live = (int)threadIdx.x < n;
+    if (live) x = I::unpark(cx, pool[threadIdx.x], item);
+    if (!__any_sync(0xffffffffu, live)) continue;
+    for (int e = 0; e < kEpoch; ++e) {
+      const bool stepping = live && I::cond(cx, x);
+      __syncwarp();
+      if (stepping) {
+        run_step<I>(cx, x);
+      } else if (live) {
+        I::finish(cx, x, item);
+        live = false;
+      }
+      if (!__any_sync(0xffffffffu, live)) break;
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ forward kernel
 // (each kernel is a __device__ body plus a __global__ wrapper, so that a program compiled at run time can wrap the
 // same body in an `extern "C"` entry point: see tallymap_b200/lower.py)
 template <class I>
 __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items) {
   extern __shared__ __align__(16) unsigned char smem[];
+  constexpr bool kPark = park_trait<I>::value;
+  __shared__ int pool_dry;        // (parking) a claim of this block found the item counter run dry
   typename I::Ctx cx;
   I::setup(cx, P, smem);
   smem_zero(smem, I::kSmemBytes);
+  if (kPark && threadIdx.x == 0) pool_dry = 0;
   __syncthreads();
   I::stage(P, smem);
   __syncthreads();
@@ -107,6 +189,7 @@ __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items)
       const u64 t = claim_item(ctr);
       if (t >= (u64)n_items) {
         alive = false;
+        if (kPark) *static_cast<volatile int*>(&pool_dry) = 1;
       } else {
         item = ticket_item(order, t);
         x = I::start(cx, item);
@@ -114,21 +197,25 @@ __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items)
       }
     }
     if (!__any_sync(0xffffffffu, alive)) break;
+    // (parking: once the counter has run dry, the block's warps go on to the end-of-launch epochs together)
+    if (kPark && __any_sync(0xffffffffu, *static_cast<volatile int*>(&pool_dry) != 0)) break;
     // while every lane's item steps, steps run back to back without the claim and finish checks, until one ends
+    // (parking: the run also stops when the counter runs dry, so no warp of the block keeps the others waiting)
     if (__all_sync(0xffffffffu, active && I::cond(cx, x))) {
       do {
-        I::step(cx, x);
-      } while (__all_sync(0xffffffffu, I::cond(cx, x)));
+        run_step<I>(cx, x);
+      } while (__all_sync(0xffffffffu, I::cond(cx, x) && !(kPark && *static_cast<volatile int*>(&pool_dry))));
     }
     const bool stepping = alive && I::cond(cx, x);
     __syncwarp();
     if (stepping) {
-      I::step(cx, x);
+      run_step<I>(cx, x);
     } else if (alive) {
       I::finish(cx, x, item);
       active = false;
     }
   }
+  if constexpr (kPark) forward_tail<I>(cx, x, item, active);
   __syncthreads();
   I::flush(cx, smem, threadIdx.x, blockDim.x);
   finish_block<I>(cx, ctl);
@@ -525,19 +612,59 @@ struct FusedVG {
 // into the same exact tally.  F and G as for FusedVG (G's replay scratch, if it has one, is not used: Map::g of
 // G::kReplay may be any index); F::State and G::State are one type; G::adj_finish gets the final state for the
 // initial one (the walkers' pre-loop code has no VJP).
+template <class F, class G>
+struct OnePassCtx {
+  typename G::Ctx g;
+  typename F::Ctx f;
+};
+template <class F, class G>
+struct OnePassState {
+  typename G::State s;
+  typename G::Adj a;
+};
+// (the forward's optional draws and parking, carried over to the one-pass program when the forward has them: the
+// step VJP is applied before each pre-drawn step, and a parked item keeps its running cotangents)
+template <class F, class G, bool = draws_trait<F>::value>
+struct OnePassDraws {};
+template <class F, class G>
+struct OnePassDraws<F, G, true> {
+  static constexpr int kUnroll = F::kUnroll;
+  typedef typename F::Draw Draw;
+  __device__ __forceinline__ static Draw draw(const OnePassCtx<F, G>& c, const OnePassState<F, G>& st, int j) {
+    return F::draw(c.f, st.s, j);
+  }
+  __device__ __forceinline__ static void apply(const OnePassCtx<F, G>& c, OnePassState<F, G>& st, const Draw& d) {
+    G::vjp(c.g, st.s, st.a);
+    F::apply(c.f, st.s, d);
+  }
+};
+template <class F, class G, bool = park_trait<F>::value>
+struct OnePassPark {};
+template <class F, class G>
+struct OnePassPark<F, G, true> {
+  struct Parked {
+    typename F::Parked f;
+    typename G::Adj a;
+  };
+  __device__ __forceinline__ static Parked park(const OnePassCtx<F, G>& c, const OnePassState<F, G>& st, i64 item) {
+    return Parked{F::park(c.f, st.s, item), st.a};
+  }
+  __device__ __forceinline__ static OnePassState<F, G> unpark(OnePassCtx<F, G>& c, const Parked& p, i64& item) {
+    OnePassState<F, G> st;
+    st.s = F::unpark(c.f, p.f, item);
+    G::start(c.g, item);            // (the adjoint's per-item context, from the item's inputs)
+    st.a = p.a;
+    return st;
+  }
+};
+
 template <class F, class G, class Map>
-struct OnePassVG {
+struct OnePassVG : OnePassDraws<F, G>, OnePassPark<F, G> {
   static constexpr int kGSmem = (G::kSmemBytes + 15) / 16 * 16;
   static constexpr int kSmemBytes = kGSmem + F::kSmemBytes;
   enum { kConsts = Map::g(G::kConsts), kOrder = Map::g(G::kOrder), kCtl = Map::g(G::kCtl), kNBuf = Map::kNBuf };
-  struct State {
-    typename G::State s;
-    typename G::Adj a;
-  };
-  struct Ctx {
-    typename G::Ctx g;
-    typename F::Ctx f;
-  };
+  typedef OnePassState<F, G> State;
+  typedef OnePassCtx<F, G> Ctx;
   __device__ __forceinline__ static Params remap_g(const Params& P) {
     Params Q;
 #pragma unroll
