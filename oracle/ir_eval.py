@@ -30,7 +30,7 @@ from . import oracle as orc
 
 F32 = np.float32
 _MATH = {p: p for p in ("log", "exp", "sin", "cos", "atan", "asin", "acos", "tan", "sinh", "cosh", "asinh", "acosh",
-                         "atanh", "exp2", "log2", "cbrt", "erf", "erfc", "erfinv")}
+                         "atanh", "exp2", "log2", "cbrt", "erf", "erfc", "erfinv", "lgamma")}
 
 
 def _wrap32(v):
@@ -152,7 +152,7 @@ def _eval(e, a):
         return (-1 if a[0] < 0 else 0) if sh >= 32 else a[0] >> sh
     if p in _MATH:
         return F32(orc.math(_MATH[p], np.array([a[0]], np.float32))[0])
-    if p in ("pow", "atan2"):
+    if p in ("pow", "atan2", "nextafter"):
         return F32(orc.math(p, np.array([a[0]], np.float32), np.array([a[1]], np.float32))[0])
     if p == "sqrt":
         with np.errstate(all="ignore"):

@@ -209,7 +209,7 @@ def ph_grad(keys, mu_a=0.1, mu_s=10.0, ct=None, max_steps=100000, C=16, nthreads
 
 MATH_FN = {"log": 0, "exp": 1, "sin": 2, "cos": 3, "pow": 4, "atan": 5, "atan2": 6, "asin": 7, "acos": 8, "tan": 9,
            "sinh": 10, "cosh": 11, "asinh": 12, "acosh": 13, "atanh": 14, "exp2": 15, "log2": 16, "cbrt": 17,
-           "erf": 18, "erfc": 19, "erfinv": 20}
+           "erf": 18, "erfc": 19, "erfinv": 20, "nextafter": 21, "lgamma": 22}
 
 
 def math(fn, x, y=None):

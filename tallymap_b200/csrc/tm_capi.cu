@@ -576,7 +576,7 @@ int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int
 }
 
 int tm_math_eval(void* stream, int32_t fn, const float* x, const float* y, float* out, int64_t n) {
-  if (fn < 0 || fn >= tmm::kMathFns || n < 0 || (n > 0 && (!x || !out || ((fn == 4 || fn == 6) && !y))))
+  if (fn < 0 || fn >= tmm::kMathFns || n < 0 || (n > 0 && (!x || !out || ((fn == 4 || fn == 6 || fn == 21) && !y))))
     return fail(TM_EINVAL, "tallymap_b200: tm_math_eval: bad arguments");
   if (n == 0) return TM_OK;
   long long grid = (n + 255) / 256;

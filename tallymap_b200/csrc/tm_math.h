@@ -496,6 +496,107 @@ TM_HD float erfinvf(float y) {
   return with_sign(x, sign_(y));
 }
 
+// nextafter(x, y) as C's nextafterf: the f32 next to x in the direction of y (an integer step of its bits; from +-0
+// the smallest subnormal with y's sign), NaN if either is NaN, y if x == y
+TM_HD float nextafterf(float x, float y) {
+  if (isnan_(x) || isnan_(y)) return f32_nan();
+  if (x == y) return y;
+  if (x == 0.0f) return u2f((f2u(y) & 0x80000000u) | 1u);
+  const uint32_t b = f2u(x);
+  return u2f(((x < y) == (x > 0.0f)) ? b + 1u : b - 1u);
+}
+
+// ln|Gamma(x)| in double, the f32 result rounded once.  Regions (every branch in double, IEEE operations only):
+//   [1.5, 2.5)   lgamma(2 + t) = (1 - euler_gamma) t + sum_{k=2..31} (-1)^k (zeta(k) - 1) t^k / k, |t| <= 1/2
+//                (the Taylor series about 2; its terms fall as 4^-k, truncation below 2e-18 of the first)
+//   [0.5, 1.5)   lgamma(1 + t) = lgamma(2 + t) - log1p(t)
+//   [2.5, 10)    lgamma(x) = lgamma(x - n) + log((x - 1) ... (x - n)), x - n in [1.5, 2.5)
+//   [10, inf)    Stirling: (x - 1/2) log x - x + log(2 pi) / 2 + sum_{k=1..8} B_2k / (2k (2k - 1) x^(2k - 1))
+//                (the next term is below 2e-18 at x = 10)
+//   (-inf, 0.5)  reflection: log(pi / |sin(pi x)|) - lgamma(1 - x); +inf at 0 and the negative integers
+TM_HD double lgamma_series2(double t) {   // lgamma(2 + t), |t| <= 1/2
+  double p = -1.5021384080754142e-11;
+  p = p * t + 3.104424774732227e-11;
+  p = p * t + -6.422964563838102e-11;
+  p = p * t + 1.3304764374244491e-10;
+  p = p * t + -2.7595228851242334e-10;
+  p = p * t + 5.731367241678861e-10;
+  p = p * t + -1.1921401405860912e-09;
+  p = p * t + 2.4836745438024785e-09;
+  p = p * t + -5.183475041970047e-09;
+  p = p * t + 1.0838659214896953e-08;
+  p = p * t + -2.2711094608943164e-08;
+  p = p * t + 4.76981016936398e-08;
+  p = p * t + -1.0043224823968102e-07;
+  p = p * t + 2.1207184805554667e-07;
+  p = p * t + -4.492469198764565e-07;
+  p = p * t + 9.551412130407415e-07;
+  p = p * t + -2.039215753801366e-06;
+  p = p * t + 4.3748667899074865e-06;
+  p = p * t + -9.439488275268398e-06;
+  p = p * t + 2.0507212775670688e-05;
+  p = p * t + -4.4926236738133156e-05;
+  p = p * t + 9.945751278180857e-05;
+  p = p * t + -0.00022315475845357936;
+  p = p * t + 0.0005096695247430426;
+  p = p * t + -0.0011927539117032612;
+  p = p * t + 0.002890510330741523;
+  p = p * t + -0.007385551028673988;
+  p = p * t + 0.020580808427784553;
+  p = p * t + -0.0673523010531981;
+  p = p * t + 0.3224670334241133;
+  return t * (0.42278433509846713939 + t * p);   // (1 - euler_gamma)
+}
+
+TM_HD double log1p_d(double t) {   // log(1 + t) for t > -1, t from an f32 difference (Goldberg's correction)
+  const double u = 1.0 + t;
+  if (u == 1.0) return t;
+  return log_pos(u) * (t / (u - 1.0));
+}
+
+TM_HD double lgamma_pos(double x) {   // x >= 0.5
+  if (x < 1.5) return lgamma_series2(x - 1.0) - log1p_d(x - 1.0);
+  if (x < 2.5) return lgamma_series2(x - 2.0);
+  if (x < 10.0) {
+    double p = 1.0, y = x;
+    while (y >= 2.5) {
+      y = y - 1.0;
+      p = p * y;
+    }
+    return lgamma_series2(y - 2.0) + log_pos(p);
+  }
+  const double r = 1.0 / x, r2 = r * r;
+  double s = -3617.0 / 122400.0;
+  s = s * r2 + 1.0 / 156.0;
+  s = s * r2 - 691.0 / 360360.0;
+  s = s * r2 + 1.0 / 1188.0;
+  s = s * r2 - 1.0 / 1680.0;
+  s = s * r2 + 1.0 / 1260.0;
+  s = s * r2 - 1.0 / 360.0;
+  s = s * r2 + 1.0 / 12.0;
+  return ((x - 0.5) * log_pos(x) - x) + (0.91893853320467274178 + s * r);
+}
+
+TM_HD double sinpi_abs(double r) {   // |sin(pi r)| for |r| <= 1
+  double a = r < 0.0 ? -r : r;
+  if (a > 0.5) a = 1.0 - a;
+  if (a <= 0.25) return sin_core(3.14159265358979311600 * a);
+  return cos_core(3.14159265358979311600 * (0.5 - a));
+}
+
+TM_HD float lgammaf(float xf) {
+  if (isnan_(xf)) return xf;
+  if (isinf_(xf)) return f32_inf();
+  const double x = (double)xf;
+  if (x >= 0.5) return to_f32(lgamma_pos(x));
+  // x < 1/2: an integer (every f32 of magnitude 2^23 or more is one) is a pole
+  const double h = x * 0.5;
+  const double n2 = (double)(long long)(h < 0.0 ? h - 0.5 : h + 0.5);   // nearest integer to x / 2
+  const double r = x - 2.0 * n2;                                       // exact: x - 2 n2 in [-1, 1]
+  if (r == 0.0 || r == 1.0 || r == -1.0 || !(x > -8388608.0)) return f32_inf();
+  return to_f32(log_pos(3.14159265358979311600 / sinpi_abs(r)) - lgamma_pos(1.0 - x));
+}
+
 // the shared dispatch of tm_math_eval and the oracle's or_math: fn as tallymap_b200.lower MATH_IDS
 TM_HD float eval(int fn, float x, float y) {
   switch (fn) {
@@ -519,9 +620,11 @@ TM_HD float eval(int fn, float x, float y) {
     case 17: return cbrtf(x);
     case 18: return erff(x);
     case 19: return erfcf(x);
+    case 21: return nextafterf(x, y);
+    case 22: return lgammaf(x);
     default: return erfinvf(x);
   }
 }
-constexpr int kMathFns = 21;
+constexpr int kMathFns = 23;
 
 }  // namespace tmm

@@ -165,6 +165,25 @@ def erfinv(x):
     return _f32("erfinv", x)
 
 
+def lgamma(x):
+    """jax.scipy.special.gammaln / lax.lgamma: ln|Gamma(x)| (+inf at 0 and the negative integers); it has no
+    derivative rule here, as the reference's op table has no digamma"""
+    return _f32("lgamma", x)
+
+
+def nextafter(x, y):
+    """jnp.nextafter / lax.nextafter: the float32 next to x in the direction of y (C's nextafterf); not
+    differentiable"""
+    if isinstance(x, T.Vec) or isinstance(y, T.Vec):
+        return T._vec_map2(nextafter, x, y)
+    x0 = x if isinstance(x, T.Var) else None
+    y0 = y if isinstance(y, T.Var) else None
+    x, y = T._lit(x, y0), T._lit(y, x0)
+    if x.dtype != T.F32 or y.dtype != T.F32:
+        raise T.TraceError("tallymap_b200.lang.nextafter takes float32")
+    return T._binary("nextafter", x, y)
+
+
 def logistic(x):
     """jax.nn.sigmoid / lax.logistic: 1 / (1 + exp(-x))"""
     return 1.0 / (1.0 + exp(-x))

@@ -58,7 +58,7 @@ _MATH = {"log": "tmm::logf", "exp": "tmm::expf", "sin": "tmm::sinf", "cos": "tmm
          "asin": "tmm::asinf", "acos": "tmm::acosf", "tan": "tmm::tanf", "sinh": "tmm::sinhf", "cosh": "tmm::coshf",
          "asinh": "tmm::asinhf", "acosh": "tmm::acoshf", "atanh": "tmm::atanhf", "exp2": "tmm::exp2f",
          "log2": "tmm::log2f", "cbrt": "tmm::cbrtf", "erf": "tmm::erff", "erfc": "tmm::erfcf",
-         "erfinv": "tmm::erfinvf"}
+         "erfinv": "tmm::erfinvf", "lgamma": "tmm::lgammaf"}
 # d out / d x of the unary math primitives above beyond log / exp / sin / cos, as C over the input's and the
 # output's expressions (jax's jvp rules: lax.py atan, asin, acos, tan, sinh, cosh, asinh, acosh, atanh, exp2, log2,
 # cbrt; special.py erf, erfc, erf_inv)
@@ -111,6 +111,8 @@ def c_expr(e, a):
         return f"{_MATH[p]}({a[0]})"
     if p == "atan2":
         return f"tmm::atan2f({a[0]}, {a[1]})"
+    if p == "nextafter":
+        return f"tmm::nextafterf({a[0]}, {a[1]})"
     if p == "sqrt":
         return f"tm_fsqrt({a[0]})"
     if p == "floor":
@@ -818,7 +820,7 @@ class _Rev:
         elif p == "convert":
             if x[0].dtype == T.F32 and e.outs[0].dtype == T.F32:
                 self.add(x[0], g)
-        elif p in ("floor", "round", "stop", "gather"):
+        elif p in ("floor", "round", "stop", "gather", "bitcast"):
             pass
         elif p == "rem":
             # lax.rem's transpose (jax: d/dx = 1, d/dy = -sign(x / y) * floor(|x / y|))
@@ -1359,7 +1361,7 @@ def _jvp_rule(e, a, d, out):
         return f"({a[0]} ? {db or '0.0f'} : {dc or '0.0f'})"
     if p == "convert":
         return x if e.outs[0].dtype == T.F32 and e.ins[0].dtype == T.F32 else None
-    if p in ("floor", "round", "stop", "gather"):
+    if p in ("floor", "round", "stop", "gather", "bitcast"):
         return None
     if p == "rem":
         q = f"tm_fdiv({a[0]}, {a[1]})"

@@ -848,6 +848,48 @@ def test_interp_and_table_search():
     assert np.array_equal(r[3], np.where(x < 0, np.float32(-9), want))
 
 
+def test_lgamma_nextafter():
+    """lang.lgamma (the shared double-precision lgamma, rounded once) against scipy's gammaln rounded to float32, and
+    lang.nextafter against numpy, both through the IR evaluator (which runs the shared math of the device); neither
+    has a derivative rule (the reference's op table has no digamma), so differentiating through them raises"""
+    from oracle.ir_eval import Evaluator
+    import scipy.special as sp
+
+    def item(t, x, y):
+        return t, tl.lgamma(x), tl.nextafter(x, y)
+    tr = T.trace_item(item, ["f32", "f32"], 2, {})
+    rng = np.random.default_rng(418)
+    x = np.concatenate([rng.uniform(-12, 12, 3000), np.exp(rng.uniform(-30, 80, 2000)),
+                        [0.0, -0.0, 1.0, 2.0, -3.0, 0.5, -2.5, np.inf, -np.inf, np.nan, 1e-45]]).astype(np.float32)
+    y = np.where(rng.random(len(x)) < 0.5, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32)
+    y[:5] = x[:5]
+    r = Evaluator(tr, 1).run([x, y], [])["results"]
+    lg, na = np.asarray(r[0], np.float32), np.asarray(r[1], np.float32)
+    with np.errstate(all="ignore"):
+        want = sp.gammaln(x.astype(np.float64)).astype(np.float32)
+    want = np.where(np.isneginf(x), np.float32(np.inf), want)         # (C's lgamma(-inf) = +inf)
+    ok = ~np.isnan(want)
+    assert np.array_equal(np.isnan(lg), np.isnan(want))
+    assert np.array_equal(lg[ok].view(np.uint32), want[ok].view(np.uint32))
+    wn = np.nextafter(x, y)
+    assert np.array_equal(np.isnan(na), np.isnan(wn))
+    assert np.array_equal(na[~np.isnan(wn)].view(np.uint32), wn[~np.isnan(wn)].view(np.uint32))
+    import tallymap_b200 as tm
+
+    def walk(t, x, key, a):
+        def body(c):
+            k, x, t = c
+            t = t.add("s", 0, tl.lgamma(a + x))
+            return k + 1, x + 1.0, t
+        k, x, t = tl.while_loop(lambda c: c[0] < 3, body, (0, x, t))
+        return t, k
+    f = tm.vmap(walk, outputs={"s": tm.Sum(())}, in_axes=(0, 0, None), max_steps=10)
+    L = f.lowered((np.float32([1.0, 2.0]), prng.split(prng.PRNGKey(0), 2), np.float32(0.5)))
+    assert "tmm::lgammaf" in L.fwd_source
+    with pytest.raises(lower.LowerError, match="lgamma"):
+        L.grad_program((0,))
+
+
 def test_n_active_with_spawn_is_refused():
     """n_active with a spawning program raises, as the reference's mapped call does (_api.py:530-532)"""
     from tallymap_b200 import backend as B

@@ -185,7 +185,7 @@ def test_ph_api_grad_forward_mode_option(cuda):
 
 
 @pytest.mark.parametrize("fn", ["atan", "atan2", "asin", "acos", "tan", "sinh", "cosh", "asinh", "acosh", "atanh",
-                                "exp2", "log2", "cbrt", "erf", "erfc", "erfinv"])
+                                "exp2", "log2", "cbrt", "erf", "erfc", "erfinv", "lgamma", "nextafter"])
 def test_device_special_math_bitwise_host(cuda, tmlib, orc, fn):
     """the inverse trigonometric, hyperbolic and erf family: device bitwise host over random bit patterns and
     in-domain values (NaN inputs and the signed zeros and infinities included)"""
@@ -194,7 +194,7 @@ def test_device_special_math_bitwise_host(cuda, tmlib, orc, fn):
     bits = rng.integers(0, 2 ** 32, n, dtype=np.uint64).astype(np.uint32).view(np.float32)
     dom = {"asin": (-1, 1), "acos": (-1, 1), "atanh": (-1, 1), "erfinv": (-1, 1), "acosh": (1, 50),
            "tan": (-50, 50), "sinh": (-95, 95), "cosh": (-95, 95), "exp2": (-155, 130), "erf": (-6, 6),
-           "erfc": (-6, 12)}.get(fn, (-100, 100))
+           "erfc": (-6, 12), "lgamma": (-20, 40)}.get(fn, (-100, 100))
     x = np.concatenate([bits, rng.uniform(*dom, n).astype(np.float32),
                         np.float32([0.0, -0.0, np.inf, -np.inf, np.nan, 1.0, -1.0])]).astype(np.float32)
     y = rng.permutation(x).astype(np.float32)
