@@ -600,6 +600,23 @@ def main():
                     "frac": round(tf_fwd / (f_ms / 1e3) / 1e9 / peak, 4)},
             "grad": {"kernel": cfg.grad.kernel, "achieved": round(tf_grad / (g_ms / 1e3) / 1e9, 2),
                      "frac": round(tf_grad / (g_ms / 1e3) / 1e9 / peak, 4)}}
+    if cfg.name == "ph" and roofline is not None:
+        # the photon's step mixes threefry with the shared math (log, sincos, sqrt in double) and f32 work, so its
+        # own speed of light is the probe of that step (tm_probe_issue kind 4); the threefry view stays beside it
+        p4, _ = _lib.probe_rate(_lib.PROBE_PHOTON_STEP, 1024, stream, dev)
+        tf_view = dict(roofline)
+        ms = dom[2]
+        roofline = {"bound": "issue", "kernel": dom[0], "achieved": round(steps_total / (ms / 1e3) / 1e9, 4),
+                    "peak": round(p4 / 1e9, 4), "unit": "G photon steps/s",
+                    "frac": round(steps_total / (ms / 1e3) / p4, 4), "traffic": traffic,
+                    "traffic_source": tf_view.get("traffic_source"),
+                    "peak_source": "measured: tm_probe_issue kind 4 (the photon step at full occupancy, deposit in a "
+                                   "register, no divergence from claims, no memory) on this GPU",
+                    "work": f"{steps_total} photon steps (from the per-item trip counts)",
+                    "modes": {"fwd": {"kernel": cfg.fwd.kernel,
+                                      "frac": round(steps_total / (f_ms / 1e3) / p4, 4)}},
+                    "threefry": {k: tf_view[k] for k in ("achieved", "peak", "unit", "frac", "achieved_int32_tops",
+                                                         "work")}}
     if roofline is not None and traffic is not None:
         # the memory side of the roofline: the kernel's measured DRAM bytes per launch over its time, against the
         # measured copy bandwidth (MEASURED_PEAKS.json): how far from memory-bound the path is

@@ -151,6 +151,8 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
  *   kind 1  16 FP32 instructions per iteration (8 independent multiply and add chains): the FP32 issue rate
  *   kind 2  one trial step of the Lorenz RK45 item per iteration (its own instruction mix at its own occupancy)
  *   kind 3  one trial step and one step VJP of that item per iteration (the replay's sweep mix)
+ *   kind 4  one step of the photon-slab item per iteration (its draws, path, voxel, scattering and roulette; the
+ *           deposit summed in a register)
  * (No counterpart in the reference, which reports no rooflines.) */
 int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
                    int64_t* threads_used);

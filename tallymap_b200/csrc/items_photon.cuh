@@ -378,3 +378,41 @@ struct PHVG1 : PhotonCommon {
 };
 
 }  // namespace tmb
+
+namespace tmb {
+
+// Roofline probe of this item (tm_probe_issue kind 4): `iters` photon steps per thread on register state -- the
+// draws, the path, the voxel indices and deposit value (summed into a register instead of the tally's atomics), the
+// Henyey-Greenstein scattering and the roulette -- a photon that ends being restarted at the source with the next
+// key, so every iteration is a full step; no claims, no memory traffic besides one word per thread.  Its rate at
+// full occupancy is the issue-rate speed of light of the photon step's own instruction mix.
+__global__ void __launch_bounds__(TM_BLOCK) probe_photon_kernel(u32 iters, u32* out) {
+  const u32 t = blockIdx.x * blockDim.x + threadIdx.x;
+  const float mu_t = 10.1f, frac = 0.1f / 10.1f, albedo = 10.0f / 10.1f;
+  Key key{t, 0x9e3779b9u};
+  PhotonState s{0, 0, 32.0f, 32.0f, 0.0f, 0.0f, 0.0f, 1.0f, 1.0f, true};
+  float acc = 0.0f;
+  for (u32 i = 0; i < iters; ++i) {
+    const PhotonCommon::Draws u = PhotonCommon::draws(key, s.k);
+    const float sl = PhotonCommon::path(u.u0, mu_t);
+    s.px = s.px + sl * s.dx;
+    s.py = s.py + sl * s.dy;
+    s.pz = s.pz + sl * s.dz;
+    const bool inside = PhotonCommon::in_box(s.px) && PhotonCommon::in_box(s.py) && PhotonCommon::in_box(s.pz);
+    const i32 flat = (PhotonCommon::voxel(s.px) * 64 + PhotonCommon::voxel(s.py)) * 64 + PhotonCommon::voxel(s.pz);
+    acc = acc + (inside ? s.w * frac : 0.0f) + (float)(flat & 1);
+    const float w1 = s.w * albedo;
+    PhotonCommon::scatter(s, u.u1, u.u2);
+    const bool low = w1 < 0.001f, survive = u.u3 < 0.1f;
+    s.w = low ? (survive ? w1 * 10.0f : 0.0f) : w1;
+    s.alive = inside && !(low && !survive);
+    s.k += 1;
+    if (!s.alive) {
+      key.b += 1u;
+      s = PhotonState{0, 0, 32.0f, 32.0f, 0.0f, 0.0f, 0.0f, 1.0f, 1.0f, true};
+    }
+  }
+  out[t] = __float_as_uint(acc) ^ (u32)s.k;
+}
+
+}  // namespace tmb

@@ -172,9 +172,14 @@ struct RWCommon {
   __device__ __forceinline__ static float move(float x, float u) { return x + 0.02f * (2.0f * u - 1.0f); }
 };
 
-struct RWFwd : RWCommon {
+// BLK: the block's threads.  Each 128 threads of a block add into their own privatised histogram (kSub of them),
+// so a bin's f32 partial sum takes as many additions before the flush whatever the block size (its rounding error
+// stays that of a 128-thread block's).
+template <int BLK>
+struct RWFwdT : RWCommon {
   enum { kX0, kKeys, kDrift, kConsts, kOrder, kHist, kSide, kCtl, kStats, kK, kTrunc, kNBuf };
-  static constexpr int kSmemBytes = (kNB + 2) * 4;
+  static constexpr int kSub = BLK / 128 > 1 ? BLK / 128 : 1;
+  static constexpr int kSmemBytes = kSub * (kNB + 2) * 4;
   struct Ctx {
     const float* x0;
     const uint2* keys;
@@ -194,7 +199,7 @@ struct RWFwd : RWCommon {
     c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
     c.keys = static_cast<const uint2*>(P.p[kKeys]);
     c.drift = __ldg(static_cast<const float*>(P.p[kDrift]));
-    c.sh = reinterpret_cast<float*>(smem);
+    c.sh = reinterpret_cast<float*>(smem) + (threadIdx.x / 128) * (kNB + 2);
     c.hist = static_cast<float*>(P.p[kHist]);
     c.side = static_cast<float*>(P.p[kSide]);
     c.stats = static_cast<i32*>(P.p[kStats]);
@@ -225,10 +230,10 @@ struct RWFwd : RWCommon {
     float x;
     i32 kc;
     u32 ka, kb;
-    i64 item;
+    i32 item;     // (an item index is below 2^31, the reference's limit on N)
   };
   __device__ __forceinline__ static Parked park(const Ctx& c, const State& s, i64 item) {
-    return Parked{s.x, s.kc, c.key.a, c.key.b, item};
+    return Parked{s.x, s.kc, c.key.a, c.key.b, (i32)item};
   }
   __device__ __forceinline__ static State unpark(Ctx& c, const Parked& p, i64& item) {
     c.key = Key{p.ka, p.kb};
@@ -241,19 +246,26 @@ struct RWFwd : RWCommon {
     c.trunc[item] = (s.kc >= c.M && pred(s.x)) ? 1 : 0;
   }
   __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {
-    SumPriv<kNB>::flush(reinterpret_cast<const float*>(smem), c.hist, tid, nth);
-    SumPriv<2>::flush(reinterpret_cast<const float*>(smem) + kNB, c.side, tid, nth);
+    for (int q = 0; q < kSub; ++q) {
+      const float* sh = reinterpret_cast<const float*>(smem) + q * (kNB + 2);
+      SumPriv<kNB>::flush(sh, c.hist, tid, nth);
+      SumPriv<2>::flush(sh + kNB, c.side, tid, nth);
+    }
   }
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static void epilogue(const Ctx&, int, int) {}
 };
+typedef RWFwdT<TM_BLOCK> RWFwd;
 
 // grad of <ct_hist, hist> + <ct_side, side> w.r.t. drift: the step VJP adds ct_hist[bin] * x; the side tally does
-// not depend on drift.
-struct RWGrad : RWCommon {
+// not depend on drift.  BLK: the block's threads (the layout of the threads' private exact words).
+template <int BLK>
+struct RWGradT : RWCommon {
   enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
-  static constexpr int kSmemBytes = ExactBins<1>::kSmemBytes + kNB * 4;
+  static constexpr int kBlock = BLK, kMinBlocks = BLK > 256 ? 2048 / BLK : 1;
+  typedef ExactBins<1, BLK> Bins;
+  static constexpr int kSmemBytes = Bins::kSmemBytes + kNB * 4;
     struct Ctx {
     const float* x0;
     const uint2* keys;
@@ -264,7 +276,7 @@ struct RWGrad : RWCommon {
     i32* stats;
     uint8_t* trunc;
     Key key;
-    mutable ExactPrivS<1> pv;
+    mutable ExactPrivS<1, BLK> pv;
   };
   typedef WalkState State;
   struct Adj {
@@ -278,12 +290,12 @@ struct RWGrad : RWCommon {
     c.g = static_cast<float*>(P.p[kG]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
-    c.ct = reinterpret_cast<const float*>(smem + ExactBins<1>::kSmemBytes);
-    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
+    c.ct = reinterpret_cast<const float*>(smem + Bins::kSmemBytes);
+    c.pv.bind(smem + Bins::kPrivOffset);
   }
   __device__ static void stage(const Params& P, unsigned char* smem) {
     const float* ct = static_cast<const float*>(P.p[kCtHist]);
-    float* d = reinterpret_cast<float*>(smem + ExactBins<1>::kSmemBytes);
+    float* d = reinterpret_cast<float*>(smem + Bins::kSmemBytes);
     for (int b = threadIdx.x; b < kNB; b += blockDim.x) d[b] = __ldg(&ct[b]);
   }
   __device__ static State start(Ctx& c, i64 item) {
@@ -314,12 +326,13 @@ struct RWGrad : RWCommon {
     if (c.pv.emit(0, a.ctb)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
   }
   __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {
-    ExactBins<1>::flush(c.pv, smem, c.gw, c.stats, tid);
+    Bins::flush(c.pv, smem, c.gw, c.stats, tid);
   }
   __device__ static void epilogue(const Ctx& c, int tid, int) {
-    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
+    if (tid == 0) Bins::readout(c.gw, c.g, c.stats);
   }
 };
+typedef RWGradT<TM_BLOCK> RWGrad;
 
 // ================================================================================================= value and grad
 // The fused programs (FusedVG, tm_runtime.cuh): the forward's outputs and the gradient of <ct, outputs> in one launch.
@@ -370,6 +383,7 @@ struct RWVG1Map {
   __host__ __device__ static constexpr int f(int i) { return RWVGMap::f(i); }
   __host__ __device__ static constexpr int g(int i) { return i == RWGrad::kReplay ? 0 : RWVGMap::g(i); }
 };
-typedef OnePassVG<RWFwd, RWGrad, RWVG1Map> RWVG1;
+// (1024-thread blocks, two per SM: the end-of-launch compaction gathers the items in flight of 32 warps)
+typedef OnePassVG<RWFwdT<1024>, RWGradT<1024>, RWVG1Map> RWVG1;
 
 }  // namespace tmb

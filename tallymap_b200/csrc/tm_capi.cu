@@ -70,6 +70,7 @@ void add_forward(const char* name) {
   k.fn = reinterpret_cast<const void*>(&tmb::forward_kernel<I>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
+  k.block = tmb::block_of<I>::value;
   (*g_reg)[name_id(name)] = k;
   g_names->push_back(name);
 }
@@ -155,7 +156,12 @@ int ensure_loaded(Kernel& k) {
 int occupancy(Kernel& k, int dev, int* occ) {
   auto it = k.occ.find(dev);
   if (it != k.occ.end()) { *occ = it->second; return TM_OK; }
-  if (k.smem > 48 * 1024) {
+  // a block's static shared memory (e.g. the end-of-launch compaction pool) and its dynamic shared memory together
+  // past the 48 KiB default need the opt-in
+  cudaFuncAttributes fa;
+  cudaError_t ea = cudaFuncGetAttributes(&fa, k.fn);
+  if (ea != cudaSuccess) return cuda_fail("cudaFuncGetAttributes", ea);
+  if (k.smem + fa.sharedSizeBytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
     if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
   }
@@ -552,11 +558,12 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
 
 int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
                    int64_t* threads_used) {
-  if (!out || iters < 1 || out_len < 128 || kind < 0 || kind > 3)
+  if (!out || iters < 1 || out_len < 128 || kind < 0 || kind > 4)
     return fail(TM_EINVAL, "tallymap_b200: tm_probe_issue: bad arguments");
   const void* fn = kind == 0 ? (const void*)tmb::probe_threefry_kernel
                  : kind == 1 ? (const void*)tmb::probe_fp32_kernel
-                 : kind == 2 ? (const void*)tmb::probe_ode_kernel<0> : (const void*)tmb::probe_ode_kernel<1>;
+                 : kind == 2 ? (const void*)tmb::probe_ode_kernel<0>
+                 : kind == 3 ? (const void*)tmb::probe_ode_kernel<1> : (const void*)tmb::probe_photon_kernel;
   int dev = 0, sms = 0, occ = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
@@ -569,7 +576,8 @@ int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int
   if (kind == 0) tmb::probe_threefry_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   else if (kind == 1) tmb::probe_fp32_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   else if (kind == 2) tmb::probe_ode_kernel<0><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
-  else tmb::probe_ode_kernel<1><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else if (kind == 3) tmb::probe_ode_kernel<1><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else tmb::probe_photon_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("probe kernel", e);
   if (threads_used) *threads_used = blocks * 128;
   return TM_OK;

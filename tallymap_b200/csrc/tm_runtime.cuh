@@ -98,6 +98,19 @@ __device__ __forceinline__ void finish_block(const typename I::Ctx& cx, u32* ctl
 // the block.  Once the item counter runs dry, lanes whose items ended stay idle while their warp still steps the
 // others; with parking, the block instead gathers its items in flight every kEpoch iterations and deals them to its
 // first warps, so its stepping warps stay full and the others stop issuing.
+// The block size of an ITEM's forward kernel: kBlock threads (with kMinBlocks resident blocks per SM, the launch
+// bounds' register cap) when it defines them, else TM_BLOCK (and no minimum: 0 leaves the register allocation to
+// ptxas, as launch bounds without one).  Larger blocks give the end-of-launch compaction below
+// more warps to gather items from.
+template <class T, class = void>
+struct block_of : tmstd::integral_constant<int, TM_BLOCK> {};
+template <class T>
+struct block_of<T, tmstd::void_t<decltype(T::kBlock)>> : tmstd::integral_constant<int, T::kBlock> {};
+template <class T, class = void>
+struct min_blocks_of : tmstd::integral_constant<int, 0> {};
+template <class T>
+struct min_blocks_of<T, tmstd::void_t<decltype(T::kMinBlocks)>> : tmstd::integral_constant<int, T::kMinBlocks> {};
+
 template <class T, class = void>
 struct draws_trait : tmstd::false_type {};
 template <class T>
@@ -134,7 +147,7 @@ __device__ __forceinline__ void run_step(const typename I::Ctx& cx, typename I::
 constexpr int kEpoch = 16;
 template <class I>
 __device__ __forceinline__ void forward_tail(typename I::Ctx& cx, typename I::State& x, i64& item, bool live) {
-  __shared__ typename I::Parked pool[TM_BLOCK];
+  __shared__ typename I::Parked pool[block_of<I>::value];
   __shared__ int pool_n;
   for (;;) {
     __syncthreads();                               // (the previous epoch's reads of the pool are done)
@@ -222,7 +235,8 @@ __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items)
 }
 
 template <class I>
-__global__ void __launch_bounds__(TM_BLOCK) forward_kernel(const Params P, const i64 n_items) {
+__global__ void __launch_bounds__(block_of<I>::value, min_blocks_of<I>::value)
+    forward_kernel(const Params P, const i64 n_items) {
   forward_body<I>(P, n_items);
 }
 
@@ -660,6 +674,7 @@ struct OnePassPark<F, G, true> {
 
 template <class F, class G, class Map>
 struct OnePassVG : OnePassDraws<F, G>, OnePassPark<F, G> {
+  static constexpr int kBlock = block_of<G>::value, kMinBlocks = min_blocks_of<G>::value;
   static constexpr int kGSmem = (G::kSmemBytes + 15) / 16 * 16;
   static constexpr int kSmemBytes = kGSmem + F::kSmemBytes;
   enum { kConsts = Map::g(G::kConsts), kOrder = Map::g(G::kOrder), kCtl = Map::g(G::kCtl), kNBuf = Map::kNBuf };

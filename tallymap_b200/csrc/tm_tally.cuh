@@ -9,12 +9,12 @@ namespace tmb {
 // launch's global words; the last block reads them out (backends/kernel/kernel.py:625-628: a flagged or overflowing
 // bin is NaN, counted in stats[3]).
 // Shared layout: NB x 5 u64 words, then a u32 flag per bin (rounded up to 8 bytes), then the private region
-// (kPrivOffset): word (b, j) of thread t at u64 index (b * 5 + j) * TM_BLOCK + t.  Global layout: the words, flags
-// packed after them.
-template <int NB>
+// (kPrivOffset): word (b, j) of thread t at u64 index (b * 5 + j) * BLK + t, BLK the block's threads.  Global layout:
+// the words, flags packed after them.
+template <int NB, int BLK = TM_BLOCK>
 struct ExactBins {
   static constexpr int kPrivOffset = NB * kExactWords * 8 + ((NB * 4 + 7) / 8) * 8;
-  static constexpr int kSmemBytes = kPrivOffset + NB * kExactWords * 8 * TM_BLOCK;
+  static constexpr int kSmemBytes = kPrivOffset + NB * kExactWords * 8 * BLK;
   template <class Priv>
   __device__ static void flush(Priv& pv, unsigned char* smem, u64* gw, i32* stats, int tid) {
     u64* const sw = reinterpret_cast<u64*>(smem);
@@ -56,10 +56,10 @@ struct ExactBins {
   }
 };
 
-// A thread-private exact accumulator of NB bins whose words live in the thread's slots of ExactBins<NB>'s private
-// region in shared memory (bind: the region's address), touched once per item.  Held in registers, its 5 words
-// per bin would stay live across the whole step loop and push the step's own values out to local memory.
-template <int NB>
+// A thread-private exact accumulator of NB bins whose words live in the thread's slots of ExactBins<NB, BLK>'s
+// private region in shared memory (bind: the region's address), touched once per item.  Held in registers, its 5
+// words per bin would stay live across the whole step loop and push the step's own values out to local memory.
+template <int NB, int BLK = TM_BLOCK>
 struct ExactPrivS {
   i64* w;       // this thread's word (0, 0)
   u32 flag;     // bit b: bin b saw a non-finite emit or lost a carry
@@ -67,7 +67,7 @@ struct ExactPrivS {
     w = reinterpret_cast<i64*>(region) + threadIdx.x;
     flag = 0u;
   }
-  __device__ __forceinline__ i64& at(int b, int j) const { return w[(b * kExactWords + j) * TM_BLOCK]; }
+  __device__ __forceinline__ i64& at(int b, int j) const { return w[(b * kExactWords + j) * BLK]; }
   __device__ __forceinline__ i64 word(int b, int j) const { return at(b, j); }
   __device__ __forceinline__ bool emit(int b, float v) {
     return exact_priv_emit([this](int bb, int jj) -> i64& { return at(bb, jj); }, flag, b, v);
