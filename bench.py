@@ -377,6 +377,9 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # NCCL's communicator setup on the log (its "nRanks" line shows every rank joined the one communicator)
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     N = args.items or cfg.items
     host = cfg.inputs(N, rank * N, N * world)
