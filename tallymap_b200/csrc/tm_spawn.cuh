@@ -86,7 +86,7 @@ __device__ __forceinline__ bool wait_seq(const u32* seq, u32 slot, u32 want) {
 //   start_child(Ctx&, const Child&) -> State       a popped child's pre-loop code
 //   step(const Ctx&, State&, Child& o0, Child& o1, int& n_out)   one step; up to 2 children to spawn (kept
 //                              privately, o0 runs first: an item that puts its smaller subtree in o0 keeps the
-//                              private stack shallow)
+//                              private stack at most log2 of the subtree deep)
 //   finish(const Ctx&, const State&, i64 item, bool child)   post-loop code; per-item results for roots only
 // or, with kPostSpawn = true (children spawned after the loop, tallymap/_tally.py spawn in the post-loop code):
 //   finish(const Ctx&, const State&, i64 item, bool child, Child& o0, Child& o1, int& n_out)
@@ -284,21 +284,27 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
     // what the hungry lanes wait for.  The decision is a policy: it changes no count and no termination.
     if (share_c || (++iter & 15u) == 0u)
       share_c = (i32)ld_volatile(qword(q, kQPending)) < (i32)ld_volatile(qword(q, kQHungry));
+    // o0 runs first: a lane whose item ended with this step continues with o0 itself (no round trip through the
+    // stack) and keeps o1 on its private stack; otherwise o1 then o0 go on the stack, so o0 is on top.  With the
+    // item putting its smaller subtree in o0, every entry on a lane's stack is the larger sibling of a node whose
+    // subtree at least halved on the way down, so a stack holds at most log2 of its root's subtree.
+    bool cont = false;
+    int first = 0;                   // the ring's first child: o0 (0) or o1 (1)
     if (n_out > 0) {
       spawned += (u32)n_out;
       const bool share = share_c;
-      int ng = 0;
-      if (!share && has_room()) push(o0);
-      else ng = 1;
+      bool r0 = false, r1 = false;   // o0 / o1 go to the ring
       if (n_out > 1) {
-        if (!share && has_room()) {
-          push(o1);
-        } else {
-          if (ng == 0) o0 = o1;
-          ++ng;
-        }
+        if (!share && has_room()) push(o1);
+        else r1 = true;
       }
-      n_out = ng;                    // the children left for the ring: o0 (and o1)
+      if constexpr (!post_spawn_trait<I>::value) cont = done && !share;
+      if (!cont) {
+        if (!share && has_room()) push(o0);
+        else r0 = true;
+      }
+      first = r0 ? 0 : 1;
+      n_out = (int)r0 + (int)r1;     // the children left for the ring
     }
     const unsigned mp = __ballot_sync(0xffffffffu, n_out > 0);
     if (mp) {
@@ -328,7 +334,7 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
         if (off + j >= allowed) break;
         const u32 t = base + off + j, slot = t % Q, lap = t / Q;
         if (wait_seq(seq, slot, 2u * lap)) {
-          ring[slot] = j == 0 ? o0 : o1;
+          ring[slot] = (j == 0 && first == 0) ? o0 : o1;
           st_release(&seq[slot], 2u * lap + 1u);      // (the leaves above are visible to whoever acquires this)
           ++published;
         } else {
@@ -345,10 +351,15 @@ __device__ __forceinline__ void spawn_body(const Params& P, const i64 n_items) {
     }
     if (done) {
       if constexpr (!post_spawn_trait<I>::value) I::finish(cx, x, item, child);
-      active = false;
-      if (sn == 0 && nl == 0) {                  // busy -> idle: leave the in-flight count
-        __threadfence();
-        atomicSub(qword(q, kQFlight), 1u);
+      if (cont) {                                // (still in flight: the lane runs its own child o0 next)
+        x = I::start_child(cx, o0);
+        child = true;
+      } else {
+        active = false;
+        if (sn == 0 && nl == 0) {                // busy -> idle: leave the in-flight count
+          __threadfence();
+          atomicSub(qword(q, kQFlight), 1u);
+        }
       }
     }
   }
