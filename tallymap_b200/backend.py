@@ -209,7 +209,7 @@ RW_VG1 = ItemProgram("rw_vg_onepass", "rw_vg_onepass", pi=RW_GRAD.pi, bc=RW_GRAD
 
 # benchmark configuration 3, the photon slab (csrc/items_photon.cuh)
 PH_FWD = ItemProgram("ph_fwd", "ph_fwd", pi=(KEY,), bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32)),
-                     consts=("max_steps",), tallies=(TSpec("dep", (64, 64, 64), f64=True),),
+                     consts=("max_steps",), tallies=(TSpec("dep", (64, 64, 64)),),
                      ys=(Operand("k", (), torch.int32), Operand("truncated", (), torch.uint8)), trunc=1)
 PH_GRAD = ItemProgram("ph_grad", "ph_grad", pi=(KEY,),
                       bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32), Operand("ct_dep", (64, 64, 64), _F32)),

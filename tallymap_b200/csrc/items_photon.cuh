@@ -38,9 +38,9 @@
 // emitted into a 2-bin exact tally.
 //
 // Buffers:
-//   ph_fwd   keys u32[N,2], mu_a f32, mu_s f32, consts i32[1], order | dep f32[64^3], dep accumulator f64[64^3], ctl,
-//            stats | k i32[N], trunc u8[N]   (the deposits accumulate in f64 -- the 16^3 voxels around the source
-//            first per block in a shared f32 window -- and are rounded once to dep by the epilogue)
+//   ph_fwd   keys u32[N,2], mu_a f32, mu_s f32, consts i32[1], order | dep f32[64^3], ctl, stats | k i32[N],
+//            trunc u8[N]   (the deposits go into dep with warp-aggregated f32 atomics, each group's sum formed in
+//            f64 and rounded once; the 16^3 voxels around the source first per block into a shared f32 window)
 //   ph_grad  keys, mu_a, mu_s, ct_dep f32[64^3], consts i32[3], order | g f32[2], exact u64[11], ctl, stats |
 //            trunc u8[N], replay scratch (stored state: p, d, w; the counters are the step index, alive is true)
 #pragma once
@@ -91,7 +91,7 @@ struct PhotonCommon {
 };
 
 struct PHFwd : PhotonCommon {
-  enum { kKeys, kMuA, kMuS, kConsts, kOrder, kDep, kDep64, kCtl, kStats, kK, kTrunc, kNBuf };
+  enum { kKeys, kMuA, kMuS, kConsts, kOrder, kDep, kCtl, kStats, kK, kTrunc, kNBuf };
   // the shared-memory window of hot voxels: x, y in [32 - kW/2, 32 + kW/2), z in [0, kW) (the source is (32, 32, 0))
   static constexpr int kW = 16, kW0 = 32 - kW / 2;
   static constexpr int kSmemBytes = kW * kW * kW * 4;
@@ -100,7 +100,6 @@ struct PHFwd : PhotonCommon {
     float mu_t, albedo, frac;
     i32 M;
     float* dep;
-    double* dep64;
     i32* stats;
     i32* kout;
     uint8_t* trunc;
@@ -118,7 +117,6 @@ struct PHFwd : PhotonCommon {
     c.frac = mu_a / c.mu_t;
     c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
     c.dep = static_cast<float*>(P.p[kDep]);
-    c.dep64 = static_cast<double*>(P.p[kDep64]);
     c.stats = static_cast<i32*>(P.p[kStats]);
     c.kout = static_cast<i32*>(P.p[kK]);
     c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);
@@ -141,7 +139,7 @@ struct PHFwd : PhotonCommon {
     const i32 flat = (ix * kBox + iy) * kBox + iz;
     const bool in_win = (u32)(ix - kW0) < (u32)kW && (u32)(iy - kW0) < (u32)kW && iz < kW;
     const i32 widx = in_win ? ((ix - kW0) * kW + (iy - kW0)) * kW + iz : -1;
-    datom_warp_window(c.dep64, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
+    fatom_warp_window(c.dep, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
     const float w1 = s.w * c.albedo;
     scatter(s, u.u1, u.u2);
     const bool low = w1 < 0.001f, survive = u.u3 < 0.1f;
@@ -160,10 +158,10 @@ struct PHFwd : PhotonCommon {
       const float v = win[b];
       if (v == 0.0f) continue;
       const int ix = kW0 + b / (kW * kW), iy = kW0 + (b / kW) % kW, iz = b % kW;
-      atomicAdd(&c.dep64[(ix * kBox + iy) * kBox + iz], (double)v);
+      fatom(&c.dep[(ix * kBox + iy) * kBox + iz], v);
     }
   }
-  __device__ static void epilogue(const Ctx& c, int tid, int nth) { f64_to_f32(c.dep64, c.dep, kS, tid, nth); }
+  __device__ static void epilogue(const Ctx&, int, int) {}
 };
 
 struct PHGrad : PhotonCommon {
@@ -276,9 +274,9 @@ struct PHGrad : PhotonCommon {
 // newest first): within the float tolerance, not bitwise.  No replay scratch: the forward's cost plus a load of
 // ct_dep and four multiply-adds per step.
 //   ph_vg_onepass  keys, mu_a, mu_s, ct_dep f32[64^3], consts i32[1], order | dep f32[64^3], g f32[2],
-//                  dep accumulator f64[64^3], exact u64[11], ctl, stats | k i32[N], trunc u8[N]
+//                  exact u64[11], ctl, stats | k i32[N], trunc u8[N]
 struct PHVG1 : PhotonCommon {
-  enum { kKeys, kMuA, kMuS, kCtDep, kConsts, kOrder, kDep, kG, kDep64, kExact, kCtl, kStats, kK, kTrunc, kNBuf };
+  enum { kKeys, kMuA, kMuS, kCtDep, kConsts, kOrder, kDep, kG, kExact, kCtl, kStats, kK, kTrunc, kNBuf };
   static constexpr int kW = PHFwd::kW, kW0 = PHFwd::kW0;
   static constexpr int kXBytes = (ExactBins<2>::kSmemBytes + 15) / 16 * 16;
   static constexpr int kSmemBytes = kXBytes + PHFwd::kSmemBytes;
@@ -288,7 +286,6 @@ struct PHVG1 : PhotonCommon {
     i32 M;
     const float* ct;
     float* dep;
-    double* dep64;
     u64* gw;
     float* g;
     i32* stats;
@@ -313,7 +310,6 @@ struct PHVG1 : PhotonCommon {
     c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));
     c.ct = static_cast<const float*>(P.p[kCtDep]);
     c.dep = static_cast<float*>(P.p[kDep]);
-    c.dep64 = static_cast<double*>(P.p[kDep64]);
     c.gw = static_cast<u64*>(P.p[kExact]);
     c.g = static_cast<float*>(P.p[kG]);
     c.stats = static_cast<i32*>(P.p[kStats]);
@@ -340,7 +336,7 @@ struct PHVG1 : PhotonCommon {
     const i32 flat = (ix * kBox + iy) * kBox + iz;
     const bool in_win = (u32)(ix - kW0) < (u32)kW && (u32)(iy - kW0) < (u32)kW && iz < kW;
     const i32 widx = in_win ? ((ix - kW0) * kW + (iy - kW0)) * kW + iz : -1;
-    datom_warp_window(c.dep64, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
+    fatom_warp_window(c.dep, c.win, flat, widx, inside ? s.w * c.frac : 0.0f);
     const float cv = inside ? __ldg(&c.ct[flat]) : 0.0f;
     st.cf = st.cf + cv * s.w;
     st.ca = st.ca + (cv * c.frac) * st.tw;
@@ -368,12 +364,11 @@ struct PHVG1 : PhotonCommon {
       const float v = win[b];
       if (v == 0.0f) continue;
       const int ix = kW0 + b / (kW * kW), iy = kW0 + (b / kW) % kW, iz = b % kW;
-      atomicAdd(&c.dep64[(ix * kBox + iy) * kBox + iz], (double)v);
+      fatom(&c.dep[(ix * kBox + iy) * kBox + iz], v);
     }
   }
-  __device__ static void epilogue(const Ctx& c, int tid, int nth) {
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
     if (tid == 0) ExactBins<2>::readout(c.gw, c.g, c.stats);
-    f64_to_f32(c.dep64, c.dep, kS, tid, nth);
   }
 };
 

@@ -177,6 +177,34 @@ __device__ __forceinline__ void datom_warp_window(double* base, float* win, i32 
   else atomicAdd(&base[idx], sum);
 }
 
+// datom_warp_window for an f32 tally accumulated in place: a group's values (the lanes of the warp adding into one
+// bin in this call) are summed in f64 in ascending lane order and rounded once, then added with one f32 atomic into
+// the block's window bin widx (widx >= 0: a shared-memory f32 window of hot bins, added into the tally once per
+// block) or into the global bin idx (fatom: one red.global.add.f32, a compare-and-swap add below 2^-102).  The f64
+// group sum keeps a hot bin's per-warp addends from rounding the same way thousands of times; the global bins get one
+// f32 add per warp group, the source voxel's window one per block.  Every lane that reaches the call must make it.
+__device__ __forceinline__ void fatom_warp_window(float* base, float* win, i32 idx, i32 widx, float v) {
+  const unsigned active = __activemask();
+  const int lane = threadIdx.x & 31;
+  const bool live = v != 0.0f;
+  const unsigned peers = __match_any_sync(active, live ? idx : -1 - lane);
+  if (!live) return;
+  float sum = v;
+  if (peers != (1u << lane)) {
+    double d = 0.0;
+    unsigned rest = peers;
+    while (rest) {
+      const int src = __ffs(rest) - 1;
+      rest &= rest - 1u;
+      d = d + (double)__shfl_sync(peers, v, src);
+    }
+    if (lane != __ffs(peers) - 1) return;
+    sum = __double2float_rn(d);
+  }
+  if (widx >= 0) atomicAdd(&win[widx], sum);
+  else fatom(&base[idx], sum);
+}
+
 // the epilogue of an f64-accumulated tally: out[i] = f32(acc[i]) (round to nearest), block-wide
 __device__ __forceinline__ void f64_to_f32(const double* acc, float* out, int n, int tid, int nth) {
   for (int i = tid; i < n; i += nth) out[i] = __double2float_rn(acc[i]);
