@@ -363,6 +363,11 @@ def main():
         return reference_arm(args, rank, world)
     if args.warmup < 3:
         raise SystemExit("bench.py: at least 3 warm-up steps")
+    if world > 1:
+        # NCCL's communicator setup on the log (its INIT lines show every rank joining the one communicator); set
+        # before torch loads NCCL, which reads them once
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
     import torch
     import torch.distributed as dist
@@ -377,9 +382,6 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        # NCCL's communicator setup on the log (its "nRanks" line shows every rank joined the one communicator)
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     N = args.items or cfg.items
     host = cfg.inputs(N, rank * N, N * world)
