@@ -302,6 +302,7 @@ __device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) 
 
   enum { IDLE, COUNT, CKPT, SEG, SUB, FILL, SWEEP, DONE };
   X x, init, fin;
+  S pre;          // (V == 1) the next stored state of the sweep, loaded while the current VJP runs
   typename I::Adj adj;
   int phase = have ? IDLE : -1;   // -1: no work left for this lane
   // step counts are bounded by max_steps < 2^31 (the cap is an i32 launch constant), so 32-bit bookkeeping
@@ -340,7 +341,12 @@ __device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) 
       }
       if (phase == FILL) {
         if (a >= u * C) tape[a - u * C] = I::store(x);
-        if (a == u * C + LL - 1) { i = LL - 1; phase = SWEEP; continue; }
+        if (a == u * C + LL - 1) {
+          i = LL - 1;
+          if constexpr (V == 1) pre = tape[i];
+          phase = SWEEP;
+          continue;
+        }
         ++a;
         break;
       }
@@ -360,7 +366,12 @@ __device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) 
         LL = min(C, L - u * C);
         first = (s == 0 && u == 0);
         base = s * m + u * C;
-        if (first) { i = LL - 1; phase = SWEEP; continue; }
+        if (first) {
+          i = LL - 1;
+          if constexpr (V == 1) pre = head[i];
+          phase = SWEEP;
+          continue;
+        }
         x = I::restore(cx, ck[s], s * m);
         a = 0;
         phase = FILL;
@@ -397,15 +408,25 @@ __device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) 
     }
     __syncwarp();
     if (vjp) {
-      // up to V stored states, newest first: the loads issue together, then the VJPs run in order
       const S* const src = first ? head : tape;
-      S st[V];
+      if constexpr (V == 1) {
+        // one VJP per iteration, software-pipelined: the state for this VJP was loaded in the previous iteration
+        // (or when the sweep began), and the next one's load issues before this VJP's arithmetic, so its latency
+        // hides behind it
+        const S cur = pre;
+        if (i > 0) pre = src[i - 1];
+        I::vjp(cx, I::restore(cx, cur, base + i), adj);
+        i -= 1;
+      } else {
+        // up to V stored states, newest first: the loads issue together, then the VJPs run in order
+        S st[V];
 #pragma unroll
-      for (int v = 0; v < V; ++v) st[v] = src[i - v >= 0 ? i - v : 0];
+        for (int v = 0; v < V; ++v) st[v] = src[i - v >= 0 ? i - v : 0];
 #pragma unroll
-      for (int v = 0; v < V; ++v)
-        if (i - v >= 0) I::vjp(cx, I::restore(cx, st[v], base + i - v), adj);
-      i -= V;
+        for (int v = 0; v < V; ++v)
+          if (i - v >= 0) I::vjp(cx, I::restore(cx, st[v], base + i - v), adj);
+        i -= V;
+      }
     }
   }
   __syncthreads();
