@@ -239,6 +239,7 @@ struct ODFwd : OdeCommon {
 };
 
 struct ODGrad : OdeCommon {
+  static constexpr int kMinBlocks = 5;   // (94 registers, no spills: 5 blocks per SM instead of 4)
   enum { kSigma, kRho, kY0, kId, kBeta, kCtFinal, kCtMean, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc,
          kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads, kConstBins };

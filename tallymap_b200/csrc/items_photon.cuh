@@ -165,6 +165,7 @@ struct PHFwd : PhotonCommon {
 };
 
 struct PHGrad : PhotonCommon {
+  static constexpr int kMinBlocks = 5;   // (96 registers without the spill ptxas picks unbounded)
   enum { kKeys, kMuA, kMuS, kCtDep, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
   static constexpr int kSmemBytes = ExactBins<2>::kSmemBytes;

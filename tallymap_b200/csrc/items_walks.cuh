@@ -263,7 +263,7 @@ template <int BLK>
 struct RWGradT : RWCommon {
   enum { kX0, kKeys, kDrift, kCtHist, kCtSide, kConsts, kOrder, kG, kExact, kCtl, kStats, kTrunc, kReplay, kNBuf };
   enum { kConstM, kConstC, kConstThreads };
-  static constexpr int kBlock = BLK, kMinBlocks = BLK > 256 ? 2048 / BLK : 1;
+  static constexpr int kBlock = BLK, kMinBlocks = BLK > 256 ? 2048 / BLK : 0;
   typedef ExactBins<1, BLK> Bins;
   static constexpr int kSmemBytes = Bins::kSmemBytes + kNB * 4;
     struct Ctx {

@@ -67,7 +67,8 @@ template <class I>
 void add_forward(const char* name) {
   Kernel k;
   k.name = name;
-  k.fn = reinterpret_cast<const void*>(&tmb::forward_kernel<I>);
+  if constexpr (tmb::min_blocks_of<I>::value > 0) k.fn = reinterpret_cast<const void*>(&tmb::forward_kernel_occ<I>);
+  else k.fn = reinterpret_cast<const void*>(&tmb::forward_kernel<I>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
   k.block = tmb::block_of<I>::value;
@@ -101,7 +102,8 @@ template <class I, int V>
 void add_replay(const char* name) {
   Kernel k;
   k.name = name;
-  k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, V>);
+  if constexpr (tmb::min_blocks_of<I>::value > 0) k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel_occ<I, V>);
+  else k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, V>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
   (*g_reg)[name_id(name)] = k;

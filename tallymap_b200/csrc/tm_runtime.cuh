@@ -234,9 +234,15 @@ __device__ __forceinline__ void forward_body(const Params& P, const i64 n_items)
   finish_block<I>(cx, ctl);
 }
 
+// (two entry points: launch bounds with a minimum of resident blocks only for an ITEM that asks for one -- a
+// minimum of 0 does not always leave ptxas's register allocation as no minimum does)
+template <class I>
+__global__ void __launch_bounds__(block_of<I>::value) forward_kernel(const Params P, const i64 n_items) {
+  forward_body<I>(P, n_items);
+}
 template <class I>
 __global__ void __launch_bounds__(block_of<I>::value, min_blocks_of<I>::value)
-    forward_kernel(const Params P, const i64 n_items) {
+    forward_kernel_occ(const Params P, const i64 n_items) {
   forward_body<I>(P, n_items);
 }
 
@@ -436,6 +442,11 @@ __device__ __forceinline__ void replay_body(const Params& P, const i64 n_items) 
 
 template <class I, int V>
 __global__ void __launch_bounds__(TM_BLOCK) replay_kernel(const Params P, const i64 n_items) {
+  replay_body<I, V>(P, n_items);
+}
+template <class I, int V>
+__global__ void __launch_bounds__(TM_BLOCK, min_blocks_of<I>::value) replay_kernel_occ(const Params P,
+                                                                                       const i64 n_items) {
   replay_body<I, V>(P, n_items);
 }
 
