@@ -330,6 +330,41 @@ def parity_block(cfg, host, runs, nth, prefix=262144, longest=1024):
     return out
 
 
+def oracle_split(cfg, host, n, nth):
+    """the CPU step's parts on the first n items, timed separately (seconds): the forward, the gradient in the
+    reference's order (its checkpointed replay / tree adjoint), and -- where the GPU step runs a one-pass program --
+    the gradient by the same one-pass algorithm, so the GPU-to-CPU ratio of like algorithms can be read off"""
+    from oracle import oracle
+    h = [a[:n] for a in host]
+    parts = {}
+
+    def timed(name, f):
+        t0 = time.perf_counter()
+        f()
+        parts[name] = time.perf_counter() - t0
+    if cfg.name == "rw":
+        timed("fwd", lambda: oracle.rw_fwd(h[0], h[1], 1.0, nthreads=nth, f64acc=False))
+        timed("grad", lambda: oracle.rw_grad(h[0], h[1], 1.0, np.ones(256, np.float32), nthreads=nth))
+        timed("grad_onepass", lambda: oracle.rw_grad(h[0], h[1], 1.0, np.ones(256, np.float32), C=-1,
+                                                     nthreads=nth))
+    elif cfg.name == "q1":
+        timed("fwd", lambda: oracle.q1_fwd(h[0], h[1], 2.0, nthreads=nth, f64acc=False))
+        timed("grad", lambda: oracle.q1_grad(h[0], h[1], 2.0, np.ones(16, np.float32), nthreads=nth))
+        timed("grad_onepass", lambda: oracle.q1_grad(h[0], h[1], 2.0, np.ones(16, np.float32), C=-1, nthreads=nth))
+    elif cfg.name == "ph":
+        timed("fwd", lambda: oracle.ph_fwd(h[0], nthreads=nth, f64acc=False, libm=True))
+        timed("grad", lambda: oracle.ph_grad(h[0], nthreads=nth, libm=True))
+        timed("grad_onepass", lambda: oracle.ph_grad(h[0], C=-1, nthreads=nth, libm=True))
+    elif cfg.name == "od":
+        timed("fwd", lambda: oracle.od_fwd(*h, nthreads=nth, f64acc=False))
+        timed("grad", lambda: oracle.od_grad(*h, nthreads=nth))
+    else:
+        timed("fwd", lambda: oracle.sh_fwd(*h, nthreads=nth, f64acc=False))
+        timed("grad", lambda: oracle.sh_grad(*h, nthreads=nth))
+        timed("grad_onepass", lambda: oracle.sh_vg1(*h, nthreads=nth))
+    return {k + "_mitems_s": round(n / v / 1e6, 4) for k, v in parts.items()}
+
+
 def cpu_rate(cfg, host, target_s, nth):
     """-> (items, seconds, Mitems/s) of oracle_step on a prefix of the items sized to about target_s seconds"""
     n = min(4096, len(host[0]))
@@ -649,7 +684,10 @@ def main():
         n, dt, v = cpu_rate(cfg, host, 10.0, nth)
         cpu = {"value": round(v, 4), "unit": "Mitems/s", "cores": nth, "kind": "port",
                "sample": f"oracle port (the reference CPU kernel target's model: f32 tallies, libm): fwd + grad of "
-                         f"the first {n} items, {dt:.1f} s on {nth} OpenMP threads"}
+                         f"the first {n} items, {dt:.1f} s on {nth} OpenMP threads",
+               # the parts on the same items: forward, the reference-order gradient (the value's), and the one-pass
+               # gradient the GPU step uses (the like-for-like algorithm)
+               "split": oracle_split(cfg, host, n, nth)}
     info = _lib.kernel_info(_lib.kernel_id((fused or cfg.grad).kernel)[0])
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
