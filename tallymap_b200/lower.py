@@ -539,15 +539,48 @@ def forward_source(it, standalone=True):
     lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
     lines.append("    return s.kc < c.M && pred(c, s);")
     lines.append("  }")
+    split = _draw_split(it)
+    if split is not None:
+        # the body's draws evaluated ahead (kUnroll steps per iteration), the rest applied step by step; and the
+        # state, the saved per-item context and the item index movable to another thread (end-of-launch compaction)
+        dcode, rest, live = _draw_code(it, split)
+        lines += dcode
+        lines.append("  __device__ __forceinline__ static void apply(const Ctx& c, State& s, const Draw& d) {")
+        names = _names_loop(it, tr.carry)
+        for i in live:
+            names[i] = f"d.d{i}"
+        lines += _emit_code(rest, names, emitter)
+        lines += _assign_carry(it, names)
+        lines.append("  }")
+        lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) { apply(c, s, draw(c, s, 0)); }")
+    if not sp and not recs:
+        lines.append("  struct Parked {")
+        lines.append("    State s;")
+        lines += [f"    {CTYPE[it.vars[i].dtype]} p{i};" for i in it.saved]
+        lines.append("    i32 item;")
+        lines.append("  };")
+        lines.append("  __device__ __forceinline__ static Parked park(const Ctx& c, const State& s, i64 item) {")
+        lines.append("    Parked p;")
+        lines.append("    p.s = s;")
+        lines += [f"    p.p{i} = c.p{i};" for i in it.saved]
+        lines.append("    p.item = (i32)item;")
+        lines.append("    return p;")
+        lines.append("  }")
+        lines.append("  __device__ __forceinline__ static State unpark(Ctx& c, const Parked& p, i64& item) {")
+        lines += [f"    c.p{i} = p.p{i};" for i in it.saved]
+        lines.append("    item = p.item;")
+        lines.append("    return p.s;")
+        lines.append("  }")
     if sp:
         lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, "
                      "int& n_out) {")
-    else:
+    elif split is None:
         lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
-    names = _names_loop(it, tr.carry)
-    lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"), spawner=_spawn_code)
-    lines += _assign_carry(it, names)
-    lines.append("  }")
+    if sp or split is None:
+        names = _names_loop(it, tr.carry)
+        lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"), spawner=_spawn_code)
+        lines += _assign_carry(it, names)
+        lines.append("  }")
     if not sp:
         lines.append("  __device__ static void finish(const Ctx& c, const State& s, i64 item) {")
     elif it.post_spawns:
@@ -611,6 +644,54 @@ def _pred_fn(it):
     out.append(f"    return {_ref(tr.cond_out, names)};")
     out.append("  }")
     return out
+
+
+DRAW_UNROLL = 4      # steps drawn ahead per iteration (tm_runtime.cuh run_step) when the body's draws allow it
+_DRAW_PRIMS = ("threefry", "bits", "uniform01")
+
+
+def _draw_split(it):
+    """The body's equations that depend only on the per-item context (the saved pre-loop values), the broadcast
+    operands, literals and the step counters (carries equal to the step index): their values at step kc + j are
+    known before step kc runs, so the runtime can evaluate several steps' worth together (independent threefry
+    chains; tm_runtime.cuh, run_step).  -> (draw equations, the other equations, ids of draw values the others or
+    the carry update read) or None when the draws hold no threefry (nothing worth drawing ahead)."""
+    tr = it.tr
+    if it.spawns or tr.records:
+        return None
+    fixed = set(it.saved) | set(it.bc_ids) | {tr.carry[j].id for j in it.counter}
+    draws, rest, dset = [], [], set()
+    for e in tr.body:
+        ok = e.prim not in ("emit", "spawn", "append") and \
+            all(not isinstance(x, T.Var) or x.id in fixed or x.id in dset for x in e.ins)
+        if ok:
+            draws.append(e)
+            dset |= _ids(e.outs)
+        else:
+            rest.append(e)
+    if not any(e.prim in _DRAW_PRIMS for e in draws):
+        return None
+    live = sorted(dset & (_uses(rest) | _ids(tr.body_out)))
+    return draws, rest, live
+
+
+def _draw_code(it, split):
+    """the ITEM's kUnroll, Draw, draw(c, s, j) and apply(c, s, d) (step == apply(draw(0)))"""
+    tr = it.tr
+    draws, rest, live = split
+    out = [f"  static constexpr int kUnroll = {DRAW_UNROLL};", "  struct Draw {"]
+    out += [f"    {CTYPE[it.vars[i].dtype]} d{i};" for i in live] or ["    int unused;"]
+    out.append("  };")
+    out.append("  __device__ __forceinline__ static Draw draw(const Ctx& c, const State& s, int j) {")
+    names = _names_loop(it, tr.carry)
+    for jc in it.counter:          # a step counter at step kc + j: its value now plus j
+        names[tr.carry[jc].id] = f"(i32)((u32)s.c{jc} + (u32)j)"
+    out += _emit_code(draws, names, lambda *a: "")
+    out.append("    Draw d;")
+    out += [f"    d.d{i} = {names[i]};" for i in live]
+    out.append("    return d;")
+    out.append("  }")
+    return out, rest, live
 
 
 def _assign_carry(it, names, state="s"):
