@@ -69,6 +69,11 @@ int tm_compile_register(int64_t id, const char* source, const char* include_dir,
 int tm_compile(const char* source, const char* include_dir, int32_t block, int32_t flags, void* out, size_t cap,
                size_t* n);
 
+/* Bytes of one stored loop state in a built-in replay program's scratch (the size the host multiplies by the states
+ * per thread and the threads to allocate it; 0 for a program with no replay scratch).  No device access.
+ * (No counterpart in the reference: its scratch sizes come from the generated source's layout.) */
+int tm_kernel_state_bytes(int64_t id, int32_t* bytes);
+
 /* Resources of a kernel on the current device: out[7] = registers per thread, local bytes per thread, static
  * shared bytes per block, resident blocks per SM, SMs, max resident threads per SM, block size.
  * Replaces: tallymap_kernel_info (backends/kernel/shim.cc:147-155). */

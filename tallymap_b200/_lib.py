@@ -97,6 +97,7 @@ def lib():
         L.tm_kernel_name.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p)]
         L.tm_register.argtypes = [i64, P, ctypes.c_size_t, ctypes.c_char_p, i32, i32, i32]
         L.tm_kernel_info.argtypes = [i64, ctypes.POINTER(ctypes.c_longlong)]
+        L.tm_kernel_state_bytes.argtypes = [i64, ctypes.POINTER(i32)]
         L.tm_launch.argtypes = [i64, P, ctypes.POINTER(P), i32, i32, ctypes.POINTER(ctypes.c_size_t), i32, i32, i64,
                                 ctypes.POINTER(i32)]
         L.tm_check_status.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
@@ -122,6 +123,7 @@ def check(rc):
 
 # the symbols include/tallymap_b200.h declares (tests check the library exports each one)
 EXPORTS = ("tm_abi_version", "tm_last_error", "tm_kernel_id", "tm_kernel_name", "tm_register", "tm_kernel_info",
+           "tm_kernel_state_bytes",
            "tm_launch", "tm_check_status", "tm_exact_combine", "tm_exact_scatter", "tm_exact_scatter_noalloc",
            "tm_probe_threefry", "tm_probe_issue", "tm_ffi_available", "tm_math_eval", "tm_tree_generations",
            "tm_compile_register", "tm_compile")

@@ -215,7 +215,7 @@ PH_GRAD = ItemProgram("ph_grad", "ph_grad", pi=(KEY,),
                       bc=(Operand("mu_a", (), _F32), Operand("mu_s", (), _F32), Operand("ct_dep", (64, 64, 64), _F32)),
                       consts=("max_steps", "rev_checkpoints", "replay_threads"),
                       tallies=(TSpec("ct_mu", (2,), exact=True),),
-                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=28)
+                      ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=32)
 
 # benchmark configuration 4, the Lorenz RK45 ensemble (csrc/items_ode.cuh); "bins3": the final tally's 3N bins
 OD_PI = (Operand("sigma", (), _F32), Operand("rho", (), _F32), Operand("y0", (3,), _F32),

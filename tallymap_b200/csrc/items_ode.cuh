@@ -263,7 +263,8 @@ struct ODGrad : OdeCommon {
     V3 cy, ck1;
     float cb;
   };
-  struct Stored {
+  // (16-byte aligned, 32 bytes: a state moves as two 128-bit accesses, not eight 32-bit ones that throttle the LSU)
+  struct __align__(16) Stored {
     float tt, h;
     V3 y, k1;
   };

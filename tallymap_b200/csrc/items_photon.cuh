@@ -185,8 +185,9 @@ struct PHGrad : PhotonCommon {
   struct Adj {
     float ct_w, ct_frac, ct_albedo;
   };
-  struct Stored {
-    float px, py, pz, dx, dy, dz, w;
+  // (padded to 32 bytes and 16-byte aligned: a state moves as two 128-bit accesses)
+  struct __align__(16) Stored {
+    float px, py, pz, dx, dy, dz, w, pad;
   };
   __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {
     c.keys = static_cast<const uint2*>(P.p[kKeys]);

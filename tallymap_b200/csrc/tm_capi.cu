@@ -54,6 +54,7 @@ struct Kernel {
   std::string name;
   const void* fn = nullptr;         // built-in: the __global__ function; registered: the cudaKernel_t
   int nbuf = 0, smem = 0, block = TM_BLOCK;
+  int state_bytes = 0;              // a replay program: bytes of one stored loop state in its scratch
   std::string image, note;          // registered images only
   cudaLibrary_t lib = nullptr;
   std::unordered_map<int, int> occ; // device -> resident blocks per SM
@@ -94,6 +95,7 @@ void add_vg(const char* name) {
   k.fn = reinterpret_cast<const void*>(&tmb::vg_kernel<I, V>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
+  k.state_bytes = (int)sizeof(typename I::Stored);
   (*g_reg)[name_id(name)] = k;
   g_names->push_back(name);
 }
@@ -106,6 +108,7 @@ void add_replay(const char* name) {
   else k.fn = reinterpret_cast<const void*>(&tmb::replay_kernel<I, V>);
   k.nbuf = I::kNBuf;
   k.smem = I::kSmemBytes;
+  k.state_bytes = (int)sizeof(typename I::Stored);
   (*g_reg)[name_id(name)] = k;
   g_names->push_back(name);
 }
@@ -351,6 +354,15 @@ int tm_compile(const char* source, const char* include_dir, int32_t block, int32
   if (rc) return rc;
   *n = cubin.size();
   if (out && cap >= cubin.size()) std::memcpy(out, cubin.data(), cubin.size());
+  return TM_OK;
+}
+
+int tm_kernel_state_bytes(int64_t id, int32_t* bytes) {
+  if (!bytes) return fail(TM_EINVAL, "tallymap_b200: tm_kernel_state_bytes: null argument");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Kernel* k = find(id);
+  if (!k) return fail(TM_EINVAL, "tallymap_b200: kernel id %lld is not registered", (long long)id);
+  *bytes = k->state_bytes;
   return TM_OK;
 }
 

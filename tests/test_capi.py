@@ -45,6 +45,21 @@ def test_builtin_kernels(tmlib):
         assert nbuf == p.n_args + len(layout), p.name       # the Python layout matches the kernel's
 
 
+def test_replay_state_sizes_match_the_kernels(tmlib):
+    """the host sizes each replay scratch by the program's replay_state_bytes: it must be the kernel's stored-state
+    size, or the scratch would be too small for the states the kernel writes"""
+    from tallymap_b200 import backend as B
+    checked = 0
+    for p in B.PROGRAMS.values():
+        kid, _ = tmlib.kernel_id(p.kernel)
+        n = ctypes.c_int32()
+        tmlib.check(tmlib.lib().tm_kernel_state_bytes(kid, ctypes.byref(n)))
+        if p.replay_state_bytes or n.value:
+            assert n.value == p.replay_state_bytes, p.name
+            checked += 1
+    assert checked >= 6
+
+
 def test_unknown_kernel_rejected(tmlib):
     with pytest.raises(tmlib.TallymapError, match="no built-in kernel"):
         tmlib.kernel_id("no_such_program")
