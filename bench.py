@@ -140,22 +140,25 @@ def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_ke
     VJP)/s (kind 3).  The forward runs `steps` trial steps; the replay `micro` forward step evaluations (count,
     checkpoint and fill passes) and one step VJP per trial step.  Ideal times: forward steps / P0; replay
     steps / P1 + (micro - steps) / P0.  achieved is in forward-step equivalents (a VJP pair counts P0 / P1), so
-    frac = ideal time / measured time.  Beside it the FP32 pipe: the trial steps' algorithmic f32 operations over
-    the forward time against the probe's FP32 instruction rate (kind 1)."""
+    frac = ideal time / measured time.  `micro` is replay_micro_steps: the forward evaluations of the count,
+    checkpoint and fill passes plus one per step VJP, so the forward evaluations alone are micro - steps, of which
+    `steps` pair with the VJPs (the probe's kind 3 iteration: a trial step and a step VJP).  Beside it the FP32 pipe:
+    the trial steps' algorithmic f32 operations over the forward time against the probe's FP32 instruction rate
+    (kind 1)."""
     p0, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP, 512, stream, dev)
     p1, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP_VJP, 256, stream, dev)
     pf, _ = _lib.probe_rate(_lib.PROBE_FP32, 8192, stream, dev)
     pf *= 16
     g_s, f_s = g_ms / 1e3, f_ms / 1e3
-    ideal_g = steps / p1 + max(micro - steps, 0) / p0
+    ideal_g = steps / p1 + max(micro - 2 * steps, 0) / p0
     ideal_f = steps / p0
     eq = ideal_g * p0
     return {"bound": "issue", "kernel": grad_kernel, "achieved": round(eq / g_s / 1e9, 4), "peak": round(p0 / 1e9, 4),
             "unit": "G trial-step equivalents/s", "frac": round(ideal_g / g_s, 4), "traffic": None,
             "peak_source": "measured: tm_probe_issue kind 2 (the item's trial step at full occupancy, no "
                            "divergence or memory) and kind 3 (trial step + step VJP) on this GPU",
-            "work": f"{steps} trial steps (accepted + rejected) and {micro} forward step evaluations of the replay "
-                    f"(count, checkpoint, fill), one step VJP per trial step",
+            "work": f"{steps} trial steps (accepted + rejected); the replay: {micro - steps} forward step "
+                    f"evaluations (count, checkpoint, fill) and one step VJP per trial step",
             "probe": {"p0_steps_per_s": round(p0, 1), "p1_step_vjp_per_s": round(p1, 1)},
             "modes": {"fwd": {"kernel": fwd_kernel, "achieved": round(steps / f_s / 1e9, 4),
                               "frac": round(ideal_f / f_s, 4)},
