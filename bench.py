@@ -46,13 +46,13 @@ METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per item of one launch, from the ncu captures summarised
 # under profiles/ (kernel -> (bytes per item, items in the capture)); the bench scales them to its own launch
 TRAFFIC = {
-    "rw_vg_onepass": ((52342272 + 2833664) / 4194304, 4194304),
-    "ph_vg_onepass": ((36617472 + 297728) / 4194304, 4194304),
+    "rw_vg_onepass": ((13003008 + 0) / 1048576, 1048576),
+    "ph_vg_onepass": ((9116416 + 512) / 1048576, 1048576),
     "rw_vg": ((38916657408 + 37082540288) / 4194304, 4194304),
     "rw_grad": ((5.241173e9 + 6.034955e9) / 1048576, 1048576),
     "rw_fwd": ((53075712 + 3524096) / 4194304, 4194304),
     "ph_fwd": ((10.557440e6 + 0.0) / 1048576, 1048576),
-    "od_grad": ((2.976084e9 + 3.093681e9) / 262144, 262144),
+    "od_grad": ((3.060892e9 + 3.133417e9) / 262144, 262144),
     "od_fwd": ((0.009466e9 + 0.0) / 262144, 262144),
 }
 
