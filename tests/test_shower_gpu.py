@@ -123,17 +123,22 @@ def test_sh_tree_grad_poison(cuda, orc, how):
 
 
 def test_sh_tree_grad_full_size(cuda, orc):
-    """N = 1,048,576 roots (~10^9 recorded children): repeatable bitwise, energy-conserving E cotangents"""
+    """N = 1,048,576 roots (~10^9 recorded children): the tree adjoint against the oracle's post-order traversal of
+    every root -- each root's E and depth cotangents and the X0 cotangent (an exact tally over all roots) bitwise --,
+    repeatable bitwise, energy-conserving E cotangents"""
     inp = orc.sh_inputs(1048576)
-    a = gpu_sh_grad(inp)
-    b = gpu_sh_grad(inp)
+    ct = np.random.default_rng(1048576).uniform(0.5, 1.5, 512).astype(np.float32)
+    a = gpu_sh_grad(inp, ct=ct)
+    b = gpu_sh_grad(inp, ct=ct)
     assert not a["poisoned"] and a["mismatch"] == 0
     assert np.array_equal(a["ct_E"].view(np.uint32), b["ct_E"].view(np.uint32))
     assert np.array_equal(a["ct_X0"].view(np.uint32), b["ct_X0"].view(np.uint32))
-    assert np.median(np.abs(a["ct_E"] - 1.0)) < 1e-5
-    idx = np.random.default_rng(0).choice(1048576, 64, replace=False)
-    ref = orc.sh_grad(inp[0][idx], inp[1][idx], inp[2][idx])
-    assert np.array_equal(a["ct_E"][idx].view(np.uint32), ref["g_E"].view(np.uint32))
+    ref = orc.sh_grad(*inp, ct_dep=ct)
+    assert np.array_equal(a["ct_E"].view(np.uint32), ref["g_E"].view(np.uint32))
+    assert np.array_equal(a["ct_depth"].view(np.uint32), ref["g_depth"].view(np.uint32))
+    assert np.array_equal(a["ct_X0"].view(np.uint32), ref["g_X0"].view(np.uint32))
+    e = gpu_sh_grad(inp)
+    assert np.median(np.abs(e["ct_E"] - 1.0)) < 1e-5
 
 
 # ---------------------------------------------------------------------------------------------- one pass
