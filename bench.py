@@ -390,6 +390,9 @@ def main():
     ap.add_argument("--items", type=int, default=None, help="items per GPU (default: the configuration's N)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the per-item parity check against the oracle")
+    ap.add_argument("--index-order", action="store_true",
+                    help="(the shower) claim roots in index order instead of largest energy first (the argsort "
+                         "value_and_grad and the forward run inside the timed step)")
     ap.add_argument("--unfused", action="store_true", help="time the step as a forward and a replay launch")
     ap.add_argument("--exact-order", action="store_true",
                     help="time the fused replay (the reverse program's summation order, bitwise) instead of the "
@@ -437,8 +440,11 @@ def main():
     ntal = len(cfg.fwd.tallies)
     tree_info = {}
 
+    # the claim order the public API gives the launch (the shower: roots largest energy first), computed every step
+    claim = None if args.index_order else tm.FAMILIES[FAM[cfg.name]].claim_order
+
     def fwd():
-        out = B.run(cfg.fwd, pi, bc, consts=(cfg.max_steps,), out=fo)
+        out = B.run(cfg.fwd, pi, bc, consts=(cfg.max_steps,), out=fo, order=claim(pi) if claim else None)
         if world > 1:
             parallel.all_reduce_sums(out[:ntal + 1])
         return out
@@ -476,7 +482,8 @@ def main():
 
     def vg():
         if sh_vg:
-            r = B.sh_value_and_grad(pi, bc[0], ct[0], max_steps=cfg.max_steps, out=vo)
+            r = B.sh_value_and_grad(pi, bc[0], ct[0], max_steps=cfg.max_steps, out=vo,
+                                    order=claim(pi) if claim else None)
             if world > 1:
                 parallel.all_reduce_sums([r["dep"], r["count"], r["stats"]])
             return r

@@ -106,6 +106,8 @@ class Family:
                                                               # carry: step VJPs summed as the forward runs)
     onepass_grad: bool = False   # grad(exact_order=False) runs the one-pass launch: it is forward mode, while the
                                  # replay re-runs the forward
+    claim_order: object = None   # pi -> an int32 permutation of the items, the order the launch claims them in (a
+                                 # scheduling hint: it moves no result to another item or tally)
 
 
 FAMILIES = {
@@ -117,7 +119,9 @@ FAMILIES = {
                      onepass_grad=True),
     "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
-    "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000, onepass_grad=True),
+    # (roots claimed largest energy first: a root's subtree grows with its energy, so the launch's tail is small trees)
+    "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000, onepass_grad=True,
+                     claim_order=lambda pi: B.energy_order(pi[0])),
 }
 
 
@@ -170,7 +174,12 @@ class Mapped:
         """the forward launch; n_active: only items i < n_active run (_api.py:466-469)"""
         pi, bc = self._split(args)
         p = self.fam.fwd
-        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.queue, n_active=n_active)
+        order = None
+        if self.fam.claim_order is not None and n_active is None:
+            # (the first per-item operand moved once, here: run takes the device tensor as it is)
+            pi = [B._dev(pi[0], torch.device("cuda", torch.cuda.current_device()), torch.float32)] + pi[1:]
+            order = self.fam.claim_order(pi)
+        out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.queue, n_active=n_active, order=order)
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
@@ -301,7 +310,8 @@ class Mapped:
         pi, bc = self._split(args)
         c = cotangents.get("dep")
         ct = torch.zeros(512, dtype=torch.float32) if c is None else c
-        r = B.sh_value_and_grad(pi, bc[0], ct, max_steps=self.max_steps, queue=self.queue)
+        order = self.fam.claim_order(pi) if self.fam.claim_order is not None else None
+        r = B.sh_value_and_grad(pi, bc[0], ct, max_steps=self.max_steps, queue=self.queue, order=order)
         p = self.fam.fwd
         trunc = r["trunc"].bool()
         n_tr = trunc.sum(dtype=torch.int32)

@@ -489,15 +489,16 @@ def record_capacity(N, record=None, device=None):
 TREE_MAX_GEN = 1024     # generations the tree adjoint takes (deeper trees: NaN gradient, counted)
 
 
-def sh_value_and_grad(pi, X0, ct_dep, max_steps=100000, queue=None, stream=None, out=None):
+def sh_value_and_grad(pi, X0, ct_dep, max_steps=100000, queue=None, stream=None, out=None, order=None):
     """the shower's forward outputs and the gradient of <ct_dep, dep> in ONE spawn launch (forward mode through
     spawn, SH_VG1), then the per-root readout of the exact words (tm_exact_combine).  d/d depth0 and d/d X0 are
     zero: depth and X0 reach the outputs only through the integer bin index (the tree adjoint gives the same +0).
     -> dict(dep, count, stats, k, trunc, g_E, g_depth, g_X0, steps: every particle's steps, the launch's work
     count) as device tensors (g_E NaN for a root whose sum overflowed; the caller poisons on truncation and dropped
-    children)"""
+    children).  order: an optional root claim order (an int32 permutation), e.g. largest energy first
+    (energy_order): it changes which thread runs a root when, no result."""
     st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
-    res = run(SH_VG1, pi, [X0, ct_dep], consts=(max_steps,), queue=queue, stream=st, out=out)
+    res = run(SH_VG1, pi, [X0, ct_dep], consts=(max_steps,), queue=queue, stream=st, out=out, order=order)
     dep, count, g_E, steps, stats, k, tr = res
     N = int(k.shape[0])
     if N:
@@ -506,6 +507,14 @@ def sh_value_and_grad(pi, X0, ct_dep, max_steps=100000, queue=None, stream=None,
                                                ctypes.c_void_p(g_E.data_ptr()), ctypes.c_void_p(stats.data_ptr())))
     return dict(dep=dep, count=count, stats=stats, k=k, trunc=tr, g_E=g_E, g_depth=torch.zeros_like(g_E),
                 g_X0=torch.zeros(1, dtype=torch.float32, device=g_E.device), steps=steps)
+
+
+def energy_order(E0):
+    """the shower's roots, largest primary energy first (int32, on E0's device): a root's subtree is proportional to
+    its energy, so claiming the largest first leaves small trees for the end of the launch (longest-processing-time
+    first, with the energy as the cost estimate); the order changes no result"""
+    E0 = E0 if isinstance(E0, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(E0, np.float32))
+    return torch.argsort(E0, descending=True).to(torch.int32)
 
 
 def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):

@@ -109,3 +109,18 @@ def test_product_path_has_no_cpu_fallback():
         assert not re.search(r"^\s*(from\s+oracle|import\s+oracle)", src, flags=re.M), f
     with pytest.raises(NotImplementedError):
         B.run(B.RW_FWD, [], [], target="cpu")
+
+
+def test_shower_claim_order_is_a_permutation():
+    """the shower's claim order: every root once, largest primary energy first (host logic; no launch)"""
+    import numpy as np
+    import torch
+    import tallymap_b200 as tm
+    from tallymap_b200 import backend as B
+    E = np.random.default_rng(5).exponential(size=1000).astype(np.float32)
+    o = B.energy_order(E).numpy()
+    assert o.dtype == np.int32 and np.array_equal(np.sort(o), np.arange(1000))
+    assert np.all(np.diff(E[o]) <= 0)
+    fo = tm.FAMILIES["shower"].claim_order([torch.from_numpy(E)])
+    assert np.array_equal(fo.numpy(), o)
+    assert all(tm.FAMILIES[n].claim_order is None for n in tm.FAMILIES if n != "shower")

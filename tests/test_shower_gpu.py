@@ -188,6 +188,30 @@ def test_sh_api_value_and_grad_onepass(cuda):
     assert int(r1.outputs["count"][0]) == int(r2.outputs["count"][0])
 
 
+def test_sh_energy_order_changes_no_result(cuda, orc):
+    """roots claimed largest energy first (what the public API gives the shower's launches) against index order: the
+    counts, trip counts, truncation flags and stats bitwise, the per-root g_E bitwise (exact sums), the deposit
+    within the float tolerance (f32 atomics in another order)"""
+    inp = orc.sh_inputs(20000)
+    order = B.energy_order(torch.from_numpy(inp[0]).cuda())
+    a = B.run(B.SH_FWD, list(inp), [np.float32(1.0)], consts=(100000,))
+    b = B.run(B.SH_FWD, list(inp), [np.float32(1.0)], consts=(100000,), order=order)
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    for x, y in zip(a[1:], b[1:]):
+        assert torch.equal(x, y)
+    assert float((a[0].double() - b[0].double()).abs().max()) <= FT * float(a[0].abs().max())
+    ct = np.random.default_rng(9).normal(size=512).astype(np.float32)
+    r1 = B.sh_value_and_grad(list(inp), np.float32(1.0), ct)
+    r2 = B.sh_value_and_grad(list(inp), np.float32(1.0), ct, order=order)
+    torch.cuda.synchronize()
+    for k in ("count", "stats", "k", "trunc"):
+        assert torch.equal(r1[k], r2[k]), k
+    assert torch.equal(r1["g_E"].view(torch.int32), r2["g_E"].view(torch.int32))
+    assert torch.equal(r1["g_E"].view(torch.int32),
+                       torch.from_numpy(orc.sh_vg1(*inp, ct_dep=ct)["g_E"].view(np.int32)).cuda())
+
+
 def test_sh_vg_onepass_small_queue_poisons(cuda, orc):
     """a queue too small: dropped children poison the gradient (NaN), never a silently partial one"""
     import tallymap_b200 as tm
