@@ -382,6 +382,7 @@ class MappedFn:
             raise ValueError("tallymap_b200: max_steps must be >= 1")
         self._lowered = {}
         self.last_lowered = None
+        self.last_tree = None       # a spawning item's last tree adjoint: its counters (backend.tree_adjoint info)
 
     @staticmethod
     def _spec(a, per_item):
@@ -489,7 +490,10 @@ class MappedFn:
         p = L.fwd
         out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.spawn.capacity if self.spawn else None,
                     n_active=n_active)
-        raw = B.run.last["results"]
+        return self._result(L, p, out, B.run.last["results"])
+
+    def _result(self, L, p, out, raw):
+        """the Result of a forward launch's outputs (run()'s list; raw: its buffers by name)"""
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
@@ -518,8 +522,13 @@ class MappedFn:
         """d <cotangents, outputs> / d args[wrt] for float32 operand(s) `wrt`: ONE replay launch of the generated
         adjoint.  A broadcast operand's cotangent is summed over the items (exactly); a per-item operand's is per
         item (shape (N,) or (N, n)).  -> one cotangent for one index, a tuple in `wrt`'s order for a tuple (for
-        broadcast operands only: a vector, as before); NaN when an item's replay hit max_steps."""
+        broadcast operands only: a vector, as before); NaN when an item's replay hit max_steps.  A spawning item:
+        reverse mode through spawn, the recording forward and one launch per generation (_tree)."""
         L = self.lowered(args)
+        if L.it.spawns:
+            if order is not None or n_active is not None:
+                raise ValueError("tallymap_b200: the tree adjoint of a spawning item takes no claim order or n_active")
+            return self._tree(L, args, wrt, cotangents)[1]
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
         bidx = [w for w in idx if self.in_axes[w] is None]
         pidx = [w for w in idx if self.in_axes[w] == 0]
@@ -611,7 +620,51 @@ class MappedFn:
                 if prog is not None:
                     res, ct = self._onepass(L, prog, moved, (), cotangents)
                     return res, self._per_arg(ct, where, wrt, idx)
+        L = self.lowered(moved)
+        if L.it.spawns:
+            return self._tree(L, moved, wrt, cotangents)
         return self(*moved), self.grad(*moved, wrt=wrt, cotangents=cotangents)
+
+    def _tree(self, L, args, wrt, cotangents):
+        """(Result, gradient) of a spawning item by reverse mode through spawn (tallymap/_reverse_spawn.py:233-336):
+        the recording forward (its outputs are the Result), then one adjoint launch per generation, deepest first,
+        and one over the roots (backend.tree_record, backend.tree_adjoint).  Differentiable: float32 broadcast
+        operands (their cotangents summed over every particle, exactly) and the roots' float32 per-item operands (a
+        cotangent per root).  Every gradient is NaN when the record is incomplete (a child dropped or beyond the
+        record's capacity, a tree deeper than backend.TREE_MAX_GEN generations), when a replay disagrees with the
+        record, or when a particle hit max_steps.  The counters of the last call: self.last_tree.  (With
+        cuda_math='fast' the recording and the adjoint kernels may contract multiply-adds differently, so a replay
+        can disagree with the record: a NaN gradient, never a wrong one.)"""
+        from . import lower
+        idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
+        bidx = [w for w in idx if self.in_axes[w] is None]
+        pidx = [w for w in idx if self.in_axes[w] == 0]
+        bpos, where = self._bleaves(L, bidx)
+        fo = lower._float_operands(L.it)
+        ppos = [sum(1 for ax in self.in_axes[:w] if ax == 0) for w in pidx]
+        for w, q in zip(pidx, ppos):
+            if q not in fo:
+                raise lower.LowerError(f"tallymap_b200: argument {w} is not a float32 per-item operand (no cotangent)")
+        adj = L.tree_program(bpos)
+        rec = L.rec_program()
+        pi, bc = self._split(args)
+        t = B.tree_record(rec, pi, bc, max_steps=self.max_steps, queue=self.spawn.capacity if self.spawn else None)
+        cts = []
+        for name, o in self.outputs.items():
+            if o[1] != "f32":
+                continue
+            c = cotangents.get(name)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+        r = B.tree_adjoint(adj, t, cts, max_steps=self.max_steps, rev_checkpoints=self.opts["rev_checkpoints"])
+        self.last_tree = r["info"]
+        out = t["forward"]
+        res = self._result(L, rec, out[:len(out) - 1], t["results"])     # (without the roots' newest child)
+        bad = r["poisoned"]
+        nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
+        ct = r["g"].reshape(-1)
+        got = {w: nan(ct[q]).reshape(()) if n is None else nan(ct[q:q + n]) for w, (q, n) in where.items()}
+        got.update({w: nan(r["ct_in"][fo.index(q)]) for w, q in zip(pidx, ppos)})
+        return res, (got[wrt] if isinstance(wrt, int) else tuple(got[w] for w in idx))
 
     def _onepass(self, L, prog, args, wrt, cotangents):
         pi, bc = self._split(args)

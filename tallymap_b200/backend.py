@@ -318,7 +318,9 @@ def replay_plan(p, max_steps, rev_checkpoints=None, device=None):
     """-> (C, threads, scratch bytes) of adjoint program p's replay on the current device (decided once per program,
     device, max_steps and option, so repeated launches keep their C and reuse their buffers)."""
     dev = torch.cuda.current_device() if device is None else torch.device(device).index
-    key = (p.name, dev, int(max_steps), rev_checkpoints)
+    # (keyed by the kernel and its state size, not the program's name: lowered items of the same name, or one item's
+    # programs for different operands, are different kernels whose resident threads and scratch differ)
+    key = (p.kernel, p.replay_state_bytes, p.vg_fallback, dev, int(max_steps), rev_checkpoints)
     if key not in _PLANS:
         _PLANS[key] = _replay_plan(p, max_steps, rev_checkpoints, device)
     return _PLANS[key]
@@ -415,7 +417,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         args.append(t)
     replay_bytes = 0
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
-    R = record_capacity(N, record, dev) if p.record_bytes else 0
+    R = record_capacity(N, record, dev, record_slot_bytes(p)) if p.record_bytes else 0
     known = {"max_steps": int(consts[0]) if consts else 0, "bins3": 3 * N, "queue": Q, "record": R, "items": N}
     if p.replay_state_bytes:
         C, threads, replay_bytes = replay_plan(p, known["max_steps"], rev_checkpoints, dev)
@@ -470,19 +472,26 @@ RECORD_SLOT_BYTES = 32 + 2 + 4 + 8
 _RECORD = {}
 
 
-def record_capacity(N, record=None, device=None):
+def record_slot_bytes(p):
+    """device bytes a recorded child costs recording program p: its record, its compact generation, its place in
+    the generation lists and its initial state's cotangents (a float per float leaf)"""
+    fl = sum(int(np.prod(o.shape, dtype=np.int64)) for o in p.pi if o.dtype == _F32)
+    return p.record_bytes + 2 + 4 + 4 * fl
+
+
+def record_capacity(N, record=None, device=None, slot_bytes=RECORD_SLOT_BYTES):
     if record is not None:
         R = int(record)
         if not 1 <= R < 2 ** 31:
             raise ValueError("tallymap_b200: record capacity must be in [1, 2^31)")
         return R
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    key = (int(N), dev.index)
+    key = (int(N), dev.index, int(slot_bytes))
     if key not in _RECORD:
         torch.cuda.empty_cache()             # (blocks cached by earlier calls count as free)
         free, _ = torch.cuda.mem_get_info(dev)
         _RECORD[key] = int(max(1, min(2 ** 31 - 1, max(RECORD_MIN, RECORD_PER_ROOT * int(N)),
-                                      RECORD_BUDGET_FRACTION * free // RECORD_SLOT_BYTES)))
+                                      RECORD_BUDGET_FRACTION * free // int(slot_bytes))))
     return _RECORD[key]
 
 
@@ -517,28 +526,26 @@ def energy_order(E0):
     return torch.argsort(E0, descending=True).to(torch.int32)
 
 
-def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):
-    """Reverse mode through spawn for the shower (tallymap/_reverse_spawn.py:233-336, tree_vjp): the recording
-    forward (rec_primal), the generation lists (tm_tree_generations), then one adjoint launch per generation,
-    deepest first, and one over the roots.  Each adjoint item replays its particle and injects its children's
-    initial-state cotangents (from the previous launch) at the spawn step.
-    -> dict(forward=[dep, count, stats, k, truncated] as run() returns them, ct_X0 f32[1], ct_E f32[N],
-            ct_depth f32[N], words (ct_X0's exact scratch words, for a cross-GPU combine), info={children,
-            generations, launches (the reference's count: the recording primal + one per generation + the roots'),
-            kernels (launches of this backend's kernels), record, poisoned (device bool), ...})
-    Every cotangent is NaN when the record is incomplete (a child dropped or past the record's capacity, a
-    generation deeper than TREE_MAX_GEN), when a replay disagrees with the record, or when any particle hit
-    max_steps."""
+def tree_record(p, pi, bc, max_steps=100000, queue=None, record=None, stream=None):
+    """the first half of reverse mode through spawn (tallymap/_reverse_spawn.py:85-109 rec_primal and :255-283, the
+    generation order): recording program p's launch (the forward's outputs, every child's record and generation,
+    each root's newest child), then the generation lists (tm_tree_generations).  With the default record capacity
+    too small for the tree, the (deterministic) recording runs once more with exactly the children it counted, when
+    they fit in device memory.  -> dict(forward: run()'s outputs, args, results (by name), stats, ctl, N, R (the
+    capacity), total (children spawned), n_rec (recorded), counts (host: records per generation, the last entry
+    the generations beyond TREE_MAX_GEN), offs, lists (device: record slots by generation), G (the deepest
+    generation), incomplete (a child dropped, not recorded, or too deep: the gradient is NaN))"""
     import ctypes
     dev = torch.device("cuda", torch.cuda.current_device())
     st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    slot = record_slot_bytes(p)
     for attempt in range(2):
-        fwd = run(SH_REC, pi, [X0], consts=(max_steps,), queue=queue, record=record, stream=st)
+        fwd = run(p, pi, bc, consts=(max_steps,), queue=queue, record=record, stream=st)
         last = run.last
         res, args = last["results"], last["args"]
-        R = int(last["consts"][SH_REC.consts.index("record")])
+        R = int(last["consts"][p.consts.index("record")])
         N = int(args[0].shape[0])
-        rec, root_last, stats = res["record"], res["last"], res["stats"]
+        rec, stats = res["record"], res["stats"]
         head = torch.cat([res["tree"][:1], stats.to(torch.int64)]).cpu()        # (one sync)
         total, dropped = int(head[0]), int(head[1 + STATS.index("children_dropped")])
         if total <= R or record is not None or attempt == 1 or total >= 2 ** 31:
@@ -546,12 +553,12 @@ def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_che
         # the default capacity was short: the recording is deterministic, so record again with exactly the children
         # it counted, when they fit beside what is allocated (and keep that capacity for later calls with N roots)
         free, _ = torch.cuda.mem_get_info(dev)
-        if total * RECORD_SLOT_BYTES > 0.9 * (free + rec.numel() * rec.element_size()):
+        if total * slot > 0.9 * (free + rec.numel() * rec.element_size()):
             break
-        del fwd, last, res, rec, root_last, stats
+        del fwd, last, res, rec, stats
         run.last = None
         torch.cuda.empty_cache()
-        _RECORD[(N, dev.index)] = total
+        _RECORD[(N, dev.index, slot)] = total
         record = total
     n_rec = min(total, R)
     L = _lib.lib()
@@ -567,6 +574,93 @@ def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_che
     nz = np.nonzero(cnt[:TREE_MAX_GEN])[0]
     G = int(nz.max()) if len(nz) else 0
     incomplete = total > R or dropped > 0 or cnt[TREE_MAX_GEN] > 0
+    return dict(forward=fwd, args=args, results=res, stats=stats, ctl=last["ctl"], N=N, R=R, total=total,
+                n_rec=n_rec, counts=cnt, offs=offs, lists=lists, G=G, incomplete=bool(incomplete))
+
+
+def tree_adjoint(adj, t, cts, max_steps=100000, rev_checkpoints=None, stream=None):
+    """the second half of reverse mode through spawn for a lowered item (tallymap/_reverse_spawn.py:285-336): over a
+    recorded tree t (tree_record of the item's recording program), one launch of the adjoint program adj
+    (Lowered.tree_program) per generation, deepest first, each child's initial-state cotangents going to its
+    parent's launch, then one launch over the roots.  cts: the output cotangents (adj's operands after the item's
+    broadcast operands).  -> dict(g: f32[W], the broadcast operands' cotangents summed over every particle (exact
+    sums); ct_in: [f32[N, ...] per float per-item operand], the roots' cotangents; poisoned: a device bool -- the
+    record incomplete, a replay that disagreed with the record (tree[0]) or hit max_steps (tree[1]), or an item
+    truncated or a child dropped in the forward; the caller NaN-poisons; words, stats, info)"""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    args, res, N, n_rec = t["args"], t["results"], t["N"], t["n_rec"]
+    npi = len(adj.pi)
+    nbc = len(adj.bc) - len(cts)
+    ins = list(args[:npi + nbc])
+    for c, o in zip(cts, adj.bc[nbc:]):
+        x = _dev(c, dev, _F32)
+        if tuple(x.shape) != tuple(o.shape):
+            raise TypeError(f"{adj.name}: cotangent {o.name} has shape {tuple(x.shape)}, expected {tuple(o.shape)}")
+        ins.append(x)
+    ins += [res["record"], res["last"]]
+    C, threads, replay_bytes = replay_plan(adj, max_steps, rev_checkpoints, dev)
+    W = adj.tallies[0].S
+    n64 = W * EXACT_WORDS + (W + 1) // 2
+    fl = sum(int(np.prod(o.shape, dtype=np.int64)) for o in adj.pi if o.dtype == _F32)
+    outs = [torch.empty(CTL_WORDS, dtype=torch.int32, device=dev), torch.empty(W, dtype=_F32, device=dev),
+            torch.empty(n64, dtype=torch.int64, device=dev), torch.empty(len(STATS), dtype=torch.int32, device=dev),
+            torch.empty(4, dtype=torch.int32, device=dev)]
+    outs += [torch.zeros((N,) + tuple(o.shape), dtype=_F32, device=dev) for o in adj.ys[:-1]]
+    outs += [torch.empty(max(n_rec, 1) * max(fl, 1), dtype=_F32, device=dev),
+             torch.zeros(N, dtype=torch.uint8, device=dev),
+             torch.empty(max(1, (replay_bytes + 15) // 16) * 4, dtype=torch.int32, device=dev)]
+    nbytes = [x.numel() * x.element_size() for x in outs]
+    kid, nbuf = kernel_ref(adj.kernel)
+    cnt, offs, lists = t["counts"], t["offs"], t["lists"]
+    launches = 0
+    if not t["incomplete"]:
+        for g in list(range(t["G"], 0, -1)) + [0]:
+            n = N if g == 0 else int(cnt[g])
+            if n == 0:
+                continue
+            cst = _consts((int(max_steps), C, threads, 1 if g == 0 else 0, max(n_rec, 1)), dev)
+            order = 0 if g == 0 else lists.data_ptr() + 4 * int(offs[g])
+            ptrs = [x.data_ptr() for x in ins] + [cst.data_ptr(), order] + [x.data_ptr() for x in outs]
+            if len(ptrs) != nbuf or nbuf != adj.buffers:
+                raise _lib.TallymapError(f"{adj.name}: {len(ptrs)} buffers for a kernel of {nbuf}")
+            # (the first launch zeroes the control words, the gradient's exact words, stats and tree counters; later
+            # launches only their control words: the exact words sum over every generation)
+            _lib.launch(kid, st, ptrs, len(ins) + 2, nbytes, 5 if launches == 0 else 1, n, flags=8)
+            launches += 1
+    if launches == 0:
+        for x in outs[:5]:
+            x.zero_()
+    g_out, tree = outs[1], outs[4]
+    fstats = t["stats"]
+    bad = (tree[0] > 0) | (tree[1] > 0) | (fstats[STATS.index("children_truncated")] > 0) | \
+        (fstats[STATS.index("children_dropped")] > 0) | outs[-2].bool().any() | bool(t["incomplete"])
+    tree_adjoint.last = dict(ctl=outs[0], fwd_ctl=t["ctl"])
+    return dict(g=g_out, ct_in=outs[5:5 + len(adj.ys) - 1], poisoned=bad, words=outs[2], stats=outs[3],
+                info=dict(children=t["total"], generations=t["G"], launches=launches + 2, kernels=launches + 4,
+                          record=t["R"], poisoned=bad, mismatch=tree[0], replay_truncated=tree[1],
+                          generation_sizes=cnt[:t["G"] + 1].tolist()))
+
+
+def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):
+    """Reverse mode through spawn for the shower (tallymap/_reverse_spawn.py:233-336, tree_vjp): the recording
+    forward (rec_primal), the generation lists (tm_tree_generations), then one adjoint launch per generation,
+    deepest first, and one over the roots.  Each adjoint item replays its particle and injects its children's
+    initial-state cotangents (from the previous launch) at the spawn step.
+    -> dict(forward=[dep, count, stats, k, truncated] as run() returns them, ct_X0 f32[1], ct_E f32[N],
+            ct_depth f32[N], words (ct_X0's exact scratch words, for a cross-GPU combine), info={children,
+            generations, launches (the reference's count: the recording primal + one per generation + the roots'),
+            kernels (launches of this backend's kernels), record, poisoned (device bool), ...})
+    Every cotangent is NaN when the record is incomplete (a child dropped or past the record's capacity, a
+    generation deeper than TREE_MAX_GEN), when a replay disagrees with the record, or when any particle hit
+    max_steps."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    rt = tree_record(SH_REC, pi, [X0], max_steps=max_steps, queue=queue, record=record, stream=st)
+    fwd, args, res, stats = rt["forward"], rt["args"], rt["results"], rt["stats"]
+    rec, root_last = res["record"], res["last"]
+    N, R, n_rec, total, G = rt["N"], rt["R"], rt["n_rec"], rt["total"], rt["G"]
+    cnt, offs, lists, incomplete = rt["counts"], rt["offs"], rt["lists"], rt["incomplete"]
 
     # the adjoint launches: [E0, depth0, keys, X0, ct_dep, record, last, consts, order] | [ctl, ct_X0, exact words,
     # stats, tree counters, ct_E, ct_depth, dx, replay scratch]
@@ -604,7 +698,7 @@ def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_che
     trunc = fwd[4]
     bad = (tree[0] > 0) | (tree[1] > 0) | (stats[2] > 0) | trunc.bool().any() | bool(incomplete)
     nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
-    tree_grad.last = dict(ctl=outs[0], fwd_ctl=last["ctl"])
+    tree_grad.last = dict(ctl=outs[0], fwd_ctl=rt["ctl"])
     return dict(forward=fwd[:5], ct_X0=nan(ctX), ct_E=nan(ctE), ct_depth=nan(ctD),
                 words=outs[2], stats=outs[3],
                 info=dict(children=total, generations=G, launches=launches + 2, kernels=launches + 4, record=R,
@@ -632,7 +726,7 @@ def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None,
     if replay_bytes is None and p.replay_state_bytes:
         replay_bytes = replay_plan(p, max_steps or 2 ** 31 - 1, None, device)[2]
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
-    R = record_capacity(N, record, device) if p.record_bytes else 0
+    R = record_capacity(N, record, device, record_slot_bytes(p)) if p.record_bytes else 0
     layout, n_zero = p.result_layout(N, replay_bytes or 0, Q, R)
     # the zeroed results (tallies, scratch accumulators, control words, stats) share ONE allocation, each at a
     # 16-byte aligned offset in layout order: Sum tallies of one dtype that follow each other in the layout are then

@@ -324,6 +324,40 @@ def _spawn_code(when_c, leaves_c):
     return "".join(st)
 
 
+def _bits(v, dt):
+    """a 4-byte value's bits as an i32 (a record word)"""
+    return f"__float_as_int({v})" if dt == T.F32 else f"(i32)({v})"
+
+
+def _from_bits(w, dt):
+    return f"__int_as_float({w})" if dt == T.F32 else (f"({w} != 0)" if dt == T.BOOL else f"({CTYPE[dt]})({w})")
+
+
+def _spawn_record_code(it, gen, last):
+    """-> spawner(when, leaves) of the recording forward (the reference's rec_primal, _reverse_spawn.py:85-109): the
+    child goes to the step's child slot as in the forward, and gets a record slot (one atomic per converged group of
+    spawning lanes) holding its leaves' bits, the spawning item's previous newest child (`prev`: the item's children
+    form a chain, newest first) and, once the child has run, its own newest child (`last`); its generation goes to the
+    compact generation array.  gen / last: C lvalues of the spawning item's generation and newest child."""
+    L = len(it.loads)
+    RS = L + 2
+
+    def spawner(when_c, leaves_c):
+        st = [f"if ({when_c}) {{ Child& o_ = n_out == 0 ? o0 : o1;"]
+        st += [f" o_.l{m} = {v};" for m, v in enumerate(leaves_c)]
+        st.append(" const unsigned m_ = __activemask(); const int ld_ = __ffs(m_) - 1; const int ln_ = threadIdx.x & 31;"
+                  " unsigned long long b_ = 0ull; if (ln_ == ld_) b_ = atomicAdd(c.tree, (unsigned long long)__popc(m_));"
+                  " b_ = __shfl_sync(m_, b_, ld_) + (unsigned long long)__popc(m_ & ((1u << ln_) - 1u));"
+                  " const i32 r_ = b_ < c.R ? (i32)b_ : -1;"
+                  f" if (r_ >= 0) {{ i32* w_ = c.rec + (i64)r_ * {RS};")
+        st += [f" w_[{m}] = {_bits(f'o_.l{m}', v.dtype)};" for m, (v, _) in enumerate(it.loads)]
+        st.append(f" w_[{L}] = {last}; w_[{L + 1}] = -1;"
+                  f" c.rgen[r_] = (unsigned short)({gen} + 1 < 65535 ? {gen} + 1 : 65535); }}")
+        st.append(f" o_.slot = r_; o_.gen = {gen} + 1; {last} = r_; ++n_out; }}")
+        return "".join(st)
+    return spawner
+
+
 def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None, spawner=None):
     """straight-line C for eqns; names: id -> C expression (updated with the locals defined here)"""
     out = []
@@ -358,12 +392,14 @@ def _ref(x, names):
 
 
 # ------------------------------------------------------------------------------------------------ forward program
-def forward_source(it, standalone=True):
+def forward_source(it, standalone=True, record=False):
     """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes); standalone=False: the
-    ITEM struct alone (for a combined program)"""
+    ITEM struct alone (for a combined program).  record (a spawning item): the recording forward of the tree adjoint
+    -- the forward's outputs plus a record of every child (_spawn_record_code) and each root's newest child"""
     tr = it.tr
     npi, nbc = len(it.pi), len(it.bc)
     sp = it.spawns
+    rec = bool(record and sp)
     lines = [('#include "tm_spawn.cuh"' if sp else "") + PRELUDE, "namespace tmb {", "struct GenFwd {"]
     # buffer indices: per-item, broadcast, consts, order | tallies, [exact words], [records], [ring sequence and
     # control words], ctl, stats | ys, [record counts], trunc, [ring]
@@ -392,20 +428,28 @@ def forward_source(it, standalone=True):
         enum.append(f"kQctl = {idx}"); idx += 1
     enum.append(f"kCtl = {idx}"); idx += 1
     enum.append(f"kStats = {idx}"); idx += 1
+    if rec:
+        enum.append(f"kTree = {idx}"); idx += 1
     for r in range(len(tr.results)):
         enum.append(f"kY{r} = {idx}"); idx += 1
     for r in range(len(recs)):
         enum.append(f"kR{r}N = {idx}"); idx += 1
     enum.append(f"kTrunc = {idx}"); idx += 1
+    if rec:
+        enum.append(f"kLast = {idx}"); idx += 1
     if sp:
         enum.append(f"kQueue = {idx}"); idx += 1
+    if rec:
+        enum.append(f"kRecord = {idx}"); idx += 1
+        enum.append(f"kRecGen = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
     if sp:
-        # a child: the per-item input leaves (4 bytes each), in the order start() loads them
-        lines.append("  enum { kConstM, kConstQ };")
+        # a child: the per-item input leaves (4 bytes each), in the order start() loads them (recording: its record
+        # slot and generation too)
+        lines.append("  enum { kConstM, kConstQ" + (", kConstR" if rec else "") + " };")
         lines.append("  struct Child { " + " ".join(f"{CTYPE[v.dtype]} l{m};" for m, (v, _) in enumerate(it.loads))
-                     + " };")
+                     + (" i32 slot; i32 gen;" if rec else "") + " };")
         if it.post_spawns:
             lines.append("  static constexpr bool kPostSpawn = true;")
     # privatised tallies
@@ -448,6 +492,9 @@ def forward_source(it, standalone=True):
         ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;", f"    i32* r{r}n;"]
     if recs:
         ctx.append("    i64 item;")
+    if rec:
+        ctx += ["    i32* rec;", "    unsigned short* rgen;", "    unsigned long long* tree;", "    i32* lastout;",
+                "    u64 R;"]
     ctx.append("  };")
     lines += ctx
     lines.append("  struct State {")
@@ -456,6 +503,8 @@ def forward_source(it, standalone=True):
         lines.append(f"    {CTYPE[v.dtype]} c{j};")
     for r in range(len(recs)):
         lines.append(f"    i32 a{r};   // records appended by the item so far")
+    if rec:
+        lines.append("    i32 me, gen, last;   // own record slot (-1: a root), generation, newest child's slot")
     lines.append("  };")
     # setup
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -483,6 +532,12 @@ def forward_source(it, standalone=True):
         lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);", f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
                   f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);",
                   f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);"]
+    if rec:
+        lines += ["    c.rec = static_cast<i32*>(P.p[kRecord]);",
+                  "    c.rgen = static_cast<unsigned short*>(P.p[kRecGen]);",
+                  "    c.tree = static_cast<unsigned long long*>(P.p[kTree]);",
+                  "    c.lastout = static_cast<i32*>(P.p[kLast]);",
+                  "    c.R = (u64)(u32)__ldg(static_cast<const i32*>(P.p[kConsts]) + kConstR);"]
     lines.append("  }")
     lines.append("  __device__ static void stage(const Params&, unsigned char*) {}")
     rindex = {rname: r for r, (rname, _) in enumerate(recs)}
@@ -531,6 +586,9 @@ def forward_source(it, standalone=True):
         lines.append("    s.kc = 0;")
         for r in range(len(recs)):
             lines.append(f"    s.a{r} = 0;")
+        if rec:
+            lines.append("    s.me = ch.slot; s.gen = ch.gen; s.last = -1;" if "start_child" in head else
+                         "    s.me = -1; s.gen = 0; s.last = -1;")
         for j, x in enumerate(tr.carry_in):
             lines.append(f"    s.c{j} = {_ref(x, names)};")
         lines.append("    return s;")
@@ -578,7 +636,8 @@ def forward_source(it, standalone=True):
         lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) {")
     if sp or split is None:
         names = _names_loop(it, tr.carry)
-        lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"), spawner=_spawn_code)
+        lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"),
+                            spawner=_spawn_record_code(it, "s.gen", "s.last") if rec else _spawn_code)
         lines += _assign_carry(it, names)
         lines.append("  }")
     if not sp:
@@ -591,10 +650,18 @@ def forward_source(it, standalone=True):
     names = _names_loop(it, tr.post_carry)
     for r in range(len(recs)):
         lines.append(f"    i32 a{r} = s.a{r};")
-    lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"), spawner=_spawn_code)
+    if rec:
+        lines.append("    i32 last_ = s.last;")
+    lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"),
+                        spawner=_spawn_record_code(it, "s.gen", "last_") if rec else _spawn_code)
     if sp:
         # a child's per-item results are discarded (tallymap/_tally.py:285-286); its truncation is counted
         lines.append("    const bool tr_ = s.kc >= c.M && pred(c, s);")
+        if rec:
+            # (the child's record gets its newest child: the head of its children's chain)
+            lines.append(f"    if (child && s.me >= 0) c.rec[(i64)s.me * {len(it.loads) + 2} + {len(it.loads) + 1}] "
+                         "= last_;")
+            lines.append("    if (!child) c.lastout[item] = last_;")
         lines.append("    if (child) { if (tr_) atomicAdd(&c.stats[kStChildrenTruncated], 1); return; }")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
@@ -824,9 +891,10 @@ class _Rev:
     """reverse-mode code for a straight-line equation list: cotangent locals, first contribution assigned, later ones
     added (jax's add_jaxvals order)"""
 
-    def __init__(self, active, indent="    ", tag="g"):
+    def __init__(self, active, indent="    ", tag="g", spawn_t=None):
         self.active, self.ct, self.lines, self.indent, self.tag = active, {}, [], indent, tag
         self.n = 0
+        self.spawn_t = spawn_t      # the transpose of a spawn (the tree adjoint), else spawns have no cotangent
 
     def add(self, x, expr):
         if not isinstance(x, T.Var) or x.id not in self.active:
@@ -842,6 +910,10 @@ class _Rev:
 
     def run(self, eqns, names, ct_tally):
         for e in reversed(eqns):
+            if e.prim == "spawn":
+                if self.spawn_t is not None:
+                    self.spawn_t(self, e, names)
+                continue
             if e.prim == "emit":
                 idx, v = e.ins
                 if isinstance(v, T.Var) and v.id in self.active and e.params["tally"] in ct_tally:
@@ -912,14 +984,50 @@ class _Rev:
             raise LowerError(f"tallymap_b200.lower: no reverse rule for {p}")
 
 
-def grad_source(it, wrt, standalone=True, wrt_pi=()):
+def _float_operands(it):
+    """positions of the per-item operands whose leaves are all float32 (the ones with cotangents)"""
+    out = []
+    for j, x in enumerate(it.pi):
+        leaves = list(x) if isinstance(x, tuple) else [x]
+        if not isinstance(x, T.Key) and all(v.dtype == T.F32 for v in leaves):
+            out.append(j)
+    return tuple(out)
+
+
+def _tree_loads(it, RS):
+    """the tree adjoint's item inputs: a root's from the per-item operands, a child's from its record's words"""
+    out = [f"    {CTYPE[v.dtype]} v{v.id};" for v, _ in it.loads]
+    out.append("    if (c.roots) {")
+    out += [f"      v{v.id} = {ld};" for v, ld in it.loads]
+    out.append("    } else {")
+    out.append(f"      const i32* w_ = c.rec + item * {RS};")
+    out += [f"      v{v.id} = {_from_bits(f'w_[{m}]', v.dtype)};" for m, (v, _) in enumerate(it.loads)]
+    out.append("    }")
+    return out
+
+
+def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     """-> (C source of the replay ITEM for d <ct, outputs> / d bc[wrt], stored-state bytes, shared-memory bytes);
     standalone=False: the ITEM struct alone, its State the forward ITEM's (GenFwd: for the one-pass program).
     wrt_pi: per-item operands (positions among them, float32 scalars or vectors) whose per-item cotangents the
     program also writes (the reference's perturbed per-item inputs, _reverse.py vjp_prog `ip`): per-item results
-    f32[N] (or f32[N, n]) before the truncation flag."""
+    f32[N] (or f32[N, n]) before the truncation flag.
+    tree (a spawning item): the adjoint launch of one generation of the tree adjoint (tallymap/_reverse_spawn.py:
+    112-166, the adjoint of the "rec" program).  Its items are a generation's record slots (the claim order is the
+    generation's list) or the roots (consts[kConstRoots]).  A spawn's transpose gives the spawned leaves the
+    cotangents of the child's initial state, which the next-deeper generation's launch wrote to dx[slot]; the
+    item's children are consumed newest first along the recorded chain, and each must hold exactly the leaves the
+    replay spawns (else tree[0] counts a mismatch: _reverse_spawn.py:22-26).  At the end a child writes its own
+    initial state's cotangents to dx[own slot], a root to the per-item results (every float per-item operand)."""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
+    if tree:
+        wrt_pi = _float_operands(it)
+    Lw = len(it.loads)
+    RS = Lw + 2                           # a record: the child's leaves, prev, last
+    fleaves = [v for v, _ in it.loads if v.dtype == T.F32]
+    fpos = {v.id: f for f, v in enumerate(fleaves)}
+    Lf = max(len(fleaves), 1)
     pl = []                               # (output q, the per-item operand's leaves)
     for j in wrt_pi:
         x = it.pi[j]
@@ -939,15 +1047,20 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
         enum.append(f"kBc{k} = {idx}"); idx += 1
     for q, (t, name, shape) in enumerate(ftal):
         enum.append(f"kCt{q} = {idx}"); idx += 1
-    for nm in ("kConsts", "kOrder", "kG", "kExact", "kCtl", "kStats"):
+    # (the tree adjoint's control words come first among its outputs: a later generation's launch zeroes them
+    # alone, while the exact words sum over every launch)
+    names_ = ("kRecord", "kRootLast", "kConsts", "kOrder", "kCtl", "kG", "kExact", "kStats", "kTree") if tree else \
+        ("kConsts", "kOrder", "kG", "kExact", "kCtl", "kStats")
+    for nm in names_:
         enum.append(f"{nm} = {idx}"); idx += 1
     for q in range(len(pl)):
         enum.append(f"kGpi{q} = {idx}"); idx += 1
-    for nm in ("kTrunc", "kReplay"):
+    for nm in (("kDx",) if tree else ()) + ("kTrunc", "kReplay"):
         enum.append(f"{nm} = {idx}"); idx += 1
     enum.append(f"kNBuf = {idx}")
     lines.append("  enum { " + ", ".join(enum) + " };")
-    lines.append("  enum { kConstM = 0, kConstC = 1, kConstThreads = 2 };")
+    lines.append("  enum { kConstM = 0, kConstC = 1, kConstThreads = 2" +
+                 (", kConstRoots = 3, kConstR = 4" if tree else "") + " };")
     # output cotangents: staged in shared memory when small
     smem = f"ExactBins<{Wx}>::kSmemBytes"
     off = 0
@@ -980,6 +1093,9 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     for i in it.saved:
         ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
     ctx.append(f"    mutable ExactPrivS<{Wx}> pv;")
+    if tree:
+        ctx += ["    const i32* rec;", "    const i32* root_last;", "    float* dx;", "    u32* tree;", "    bool roots;",
+                "    i64 R;", "    i32 last;   // the current item's newest child"]
     ctx.append("  };")
     lines += ctx
     if standalone:
@@ -1009,6 +1125,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     for i in act_saved:
         lines.append(f"    float cp{i};")
     lines.append("    bool has_post;")
+    if tree:
+        lines.append("    i32 cur;   // the next recorded child to consume, newest first")
     lines.append("  };")
     # setup / stage
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -1020,6 +1138,12 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     lines += ["    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.gw = static_cast<u64*>(P.p[kExact]);",
               "    c.g = static_cast<float*>(P.p[kG]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
     lines += [f"    c.gpi{q} = static_cast<float*>(P.p[kGpi{q}]);" for q in range(len(pl))]
+    if tree:
+        lines += ["    c.rec = static_cast<const i32*>(P.p[kRecord]);",
+                  "    c.root_last = static_cast<const i32*>(P.p[kRootLast]);",
+                  "    c.dx = static_cast<float*>(P.p[kDx]);", "    c.tree = static_cast<u32*>(P.p[kTree]);",
+                  "    c.roots = __ldg(static_cast<const i32*>(P.p[kConsts]) + kConstRoots) != 0;",
+                  "    c.R = __ldg(static_cast<const i32*>(P.p[kConsts]) + kConstR);"]
     for q, (t, name, shape) in enumerate(ftal):
         ptr, S, o = ct_tally[name]
         if o is not None:
@@ -1034,8 +1158,12 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     # start: pre-loop code without emits
     lines.append("  __device__ static State start(Ctx& c, i64 item) {")
     names = _names_pre(it)
-    for v, ld in it.loads:
-        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    if tree:
+        lines += _tree_loads(it, RS)
+        lines.append(f"    c.last = c.roots ? __ldg(&c.root_last[item]) : c.rec[item * {RS} + {Lw + 1}];")
+    else:
+        for v, ld in it.loads:
+            lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
     lines += _emit_code(tr.pre, names, None, skip_emits=True)
     for i in it.saved:
         lines.append(f"    c.p{i} = {names[i]};")
@@ -1047,7 +1175,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
     lines.append("    return s.kc < c.M && pred(c, s);")
     lines.append("  }")
-    lines.append("  __device__ static void adj_start(const Ctx&, Adj& a) {")
+    lines.append(f"  __device__ static void adj_start(const Ctx&{' c' if tree else ''}, Adj& a) {{")
     for j, a_ in enumerate(carry_act):
         if a_:
             lines.append(f"    a.cc{j} = 0.0f;")
@@ -1057,6 +1185,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     for i in act_saved:
         lines.append(f"    a.cp{i} = 0.0f;")
     lines.append("    a.has_post = false;")
+    if tree:
+        lines.append("    a.cur = c.last;")
     lines.append("  }")
     lines.append("  __device__ __forceinline__ static Stored store(const State& s) {")
     lines.append("    Stored o;")
@@ -1076,6 +1206,34 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     lines += _assign_carry(it, names)
     lines.append("  }")
     bc_pos = {it.bc[k].id: q for q, k in enumerate(wrt)}
+    nsp = [0]
+
+    def spawn_t(rev, e, names):
+        """a spawn's transpose: the recorded child's initial-state cotangents into the spawned leaves"""
+        nsp[0] += 1
+        k = nsp[0]
+        when = _ref(e.ins[0], names)
+        leaves = e.ins[1:]
+        vals = [_ref(x, names) for x in leaves]
+        took = [(f, x) for x, (v, _) in zip(leaves, it.loads) if v.dtype == T.F32
+                for f in [fpos[v.id]] if isinstance(x, T.Var) and x.id in rev.active]
+        ind = rev.indent
+        out = [f"{ind}float sd{k}_{f} = 0.0f;" for f, _ in took]
+        same = " || ".join(f"w_[{m}] != {_bits(vals[m], v.dtype)}" for m, (v, _) in enumerate(it.loads)) or "false"
+        out.append(f"{ind}if ({when}) {{")
+        out.append(f"{ind}  const i32 r_ = a.cur;")
+        out.append(f"{ind}  if (r_ < 0 || r_ >= c.R) {{")
+        out.append(f"{ind}    atomicAdd(&c.tree[0], 1u);")
+        out.append(f"{ind}  }} else {{")
+        out.append(f"{ind}    const i32* w_ = c.rec + (i64)r_ * {RS};")
+        out.append(f"{ind}    if ({same}) atomicAdd(&c.tree[0], 1u);")
+        out.append(f"{ind}    a.cur = w_[{Lw}];")
+        out += [f"{ind}    sd{k}_{f} = c.dx[(i64)r_ * {Lf} + {f}];" for f, _ in took]
+        out.append(f"{ind}  }}")
+        out.append(f"{ind}}}")
+        rev.lines += out
+        for f, x in took:
+            rev.add(x, f"sd{k}_{f}")
 
     def finish_rev(rev, state_carry, into_carry, bc_field, extra=""):
         """after a reverse run: carry cotangents (into_carry: assign a.cc from the carry variables' cotangents),
@@ -1098,7 +1256,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     lines.append("  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {")
     names = _names_loop(it, tr.carry, "at")
     lines += _emit_code(tr.body, names, None, skip_emits=True)
-    rev = _Rev(act)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None)
     for j, x in enumerate(tr.body_out):
         if carry_act[j]:
             rev.add(x, f"a.cc{j}")
@@ -1110,7 +1268,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     lines.append("  __device__ static void post_vjp(const Ctx& c, const State& fin, Adj& a) {")
     names = _names_loop(it, tr.post_carry, "fin")
     lines += _emit_code(tr.post, names, None, skip_emits=True)
-    rev = _Rev(act)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None)
     rev.run(tr.post, names, ct_tally)
     lines += rev.lines
     lines += finish_rev(rev, tr.post_carry, True, "pb")
@@ -1120,8 +1278,11 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
     # the pre-loop code's VJP, then the item's emits
     lines.append("  __device__ static void adj_finish(const Ctx& c, const State&, const State& fin, Adj& a, i64 item) {")
     names = _names_pre(it)
-    for v, ld in it.loads:
-        lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    if tree:
+        lines += _tree_loads(it, RS)
+    else:
+        for v, ld in it.loads:
+            lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
     lines += _emit_code(tr.pre, names, None, skip_emits=True)
     rev = _Rev(act, tag="h")
     for j, x in enumerate(tr.carry_in):
@@ -1137,6 +1298,16 @@ def grad_source(it, wrt, standalone=True, wrt_pi=()):
         if bid in rev.ct:
             tot = f"({tot} + {rev.ct[bid]})"
         lines.append(f"    if (c.pv.emit({q}, {tot})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
+    if tree:
+        # a child: its initial state's cotangents for its parent's launch, and its recorded children all consumed;
+        # a truncated child counts in tree[1]
+        lines.append("    if (!c.roots) {")
+        lines += [f"      c.dx[item * {Lf} + {f}] = {rev.ct.get(v.id, '0.0f')};" for f, v in enumerate(fleaves)]
+        lines.append("      if (a.cur != -1) atomicAdd(&c.tree[0], 1u);")
+        lines.append("      if (fin.kc >= c.M && pred(c, fin)) atomicAdd(&c.tree[1], 1u);")
+        lines.append("      return;")
+        lines.append("    }")
+        lines.append("    if (a.cur != -1) atomicAdd(&c.tree[0], 1u);")
     for q, leaves in enumerate(pl):
         # the per-item operand's cotangent: what the pre-loop VJP gathered into its leaves (+0 for an unused one)
         for e_, v in enumerate(leaves):
@@ -1262,9 +1433,12 @@ class Lowered:
                                ys=ys, trunc=len(ys) - 1, records=records, spawns=sp,
                                queue_leaf_bytes=4 * len(it.loads) if sp else 0)
         self.n_results = len(self.tr.results)
+        self._fwd_nbuf = nbuf
         self.grads = {}
         self.jvps = {}
         self.vgs = {}
+        self.trees = {}
+        self._rec = None
 
     def _differentiable(self, wrt):
         """a table is read-only data of the item: no cotangent or tangent flows to it"""
@@ -1347,6 +1521,58 @@ class Lowered:
             self.vgs[wrt] = prog
         return self.vgs[wrt]
 
+    def rec_program(self):
+        """the tree adjoint's recording forward (a spawning item; the reference's rec_primal): the forward's outputs,
+        plus a record of every child -- its leaves, its parent's previous child and its own newest child (i32 words,
+        record_bytes each) and its generation (uint16) -- and each root's newest child (the per-item result `last`)"""
+        from .backend import ItemProgram, Operand
+        if not self.it.spawns:
+            raise ValueError(f"tallymap_b200: item {self.name!r} does not spawn")
+        if self._rec is None:
+            it = self.it
+            src, smem = forward_source(it, record=True)
+            W = len(it.loads) + 2
+            smem = (smem + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * W * 128
+            src += f"\nstatic_assert(tmb::SpawnSmem<tmb::GenFwd>::kBytes == {smem}, \"shared-memory size\");"
+            kid = self._compile(src, self.name + "_rec", self._fwd_nbuf + 4, smem)
+            self._rec = ItemProgram(self.name + "_rec", kid, pi=self.pi, bc=self.bc,
+                                    consts=("max_steps", "queue", "record"), tallies=self.fwd.tallies,
+                                    ys=self.fwd.ys + (Operand("last", (), torch.int32),), trunc=self.fwd.trunc,
+                                    spawns=True, queue_leaf_bytes=4 * W, record_bytes=4 * W)
+        return self._rec
+
+    def tree_program(self, wrt):
+        """the tree adjoint's launch over one generation (or the roots) for d <ct, outputs> / d bc[wrt] and the roots'
+        float per-item operands (grad_source(tree=True); driven by backend.tree_adjoint).  Buffers: [pi] [bc]
+        [output cotangents] [record] [roots' newest child] [consts: max_steps, C, threads, roots, R] [order] |
+        [ctl] [g f32[W]] [exact words] [stats] [tree u32[4]: mismatches, truncated replays] [ct_in per float
+        per-item operand] [dx f32[R, float leaves]] [trunc] [replay scratch]"""
+        self._differentiable(wrt)
+        from .backend import ItemProgram, TSpec, Operand
+        if not self.it.spawns:
+            raise ValueError(f"tallymap_b200: item {self.name!r} does not spawn")
+        if self.fwd.records:
+            raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
+        wrt = tuple(wrt)
+        if wrt not in self.trees:
+            for k in wrt:
+                if self.bc[k].dtype != torch.float32:
+                    raise LowerError("tallymap_b200.lower: only float32 broadcast operands are differentiable")
+            src, stored, smem = grad_source(self.it, list(wrt), tree=True)
+            fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
+            bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
+            fo = _float_operands(self.it)
+            ys = tuple(Operand(f"ct_in{j}", self.pi[j].shape, torch.float32) for j in fo)
+            ys += (_operand("truncated", T.BOOL),)
+            nbuf = len(self.pi) + len(bc) + 2 + 2 + 5 + len(fo) + 3
+            tag = "".join(map(str, wrt))
+            kid = self._compile(src, f"{self.name}_tree{tag}", nbuf, smem)
+            self.trees[wrt] = ItemProgram(f"{self.name}_tree{tag}", kid, pi=self.pi, bc=bc,
+                                          consts=("max_steps", "rev_checkpoints", "replay_threads", "roots", "record"),
+                                          tallies=(TSpec("ct", (max(len(wrt), 1),), exact=True),), ys=ys,
+                                          trunc=len(ys) - 1, replay_state_bytes=(stored + 3) // 4 * 4, buffers=nbuf)
+        return self.trees[wrt]
+
     def grad_program(self, wrt, wrt_pi=()):
         """the reverse program for d <ct, outputs> / d bc[wrt] (wrt: positions among the broadcast operands) and, per
         item, d <ct, outputs> / d pi[wrt_pi] (positions among the per-item operands: per-item results before the
@@ -1357,8 +1583,8 @@ class Lowered:
         if self.fwd.records:
             raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
         if self.it.spawns:
-            raise NotImplementedError("tallymap_b200: reverse mode through spawn (the tree adjoint) is lowered for "
-                                      "the built-in shower only")
+            raise ValueError("tallymap_b200: a spawning item's reverse mode is the tree adjoint (rec_program, "
+                             "tree_program)")
         key = wrt if not wrt_pi else (wrt, wrt_pi)
         if key not in self.grads:
             for k in wrt:

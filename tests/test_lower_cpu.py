@@ -152,8 +152,19 @@ def test_spawn_traces_and_lowers():
     assert "start_child(Ctx& c, const Child& ch)" in src and "spawn_body<tmb::GenFwd>" in src
     names = [n for n, _, _, _ in L.fwd.result_layout(8, queue=4096)[0]]
     assert names == ["dep", "count", "queue.seq", "queue.ctl", "ctl", "stats", "y0", "truncated", "queue.ring"]
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="tree adjoint"):
         L.grad_program((0,))
+    # reverse mode through spawn: the recording forward (a record of 4 leaves + prev + last per child) and the
+    # per-generation adjoint (cotangents of the float per-item operands E and depth)
+    rec = L.rec_program()
+    assert rec.record_bytes == 24 and rec.queue_leaf_bytes == 24 and rec.consts == ("max_steps", "queue", "record")
+    names = [n for n, _, _, _ in rec.result_layout(8, queue=4096, record=64)[0]]
+    assert names == ["dep", "count", "queue.seq", "queue.ctl", "ctl", "stats", "tree", "y0", "truncated", "last",
+                     "queue.ring", "record", "record.gen"]
+    adj = L.tree_program((0,))
+    assert [y.name for y in adj.ys] == ["ct_in0", "ct_in1", "truncated"] and adj.buffers == 19
+    src = lower.grad_source(L.it, [0], tree=True)[0]
+    assert "kNBuf = 19" in src and src.count("a.cur = w_[4];") == 2 and "c.dx[item * 2 + 1]" in src
     fw = tm.vmap(spawn_walk, outputs={"Q": tm.Sum((16,)), "C": tm.Sum((16,), tm.api.torch.int32)},
                  in_axes=(0, 0, 0), max_steps=100, spawn=tm.Queue(1024))
     Lw = fw.lowered((np.zeros(4, np.int32), np.ones(4, np.float32), prng.split(prng.PRNGKey(2), 4)))
