@@ -135,6 +135,22 @@ class ItemProgram:
         return out, n_zero
 
 
+_LAYOUTS = {}
+
+
+def _layout(p, N, replay_bytes, queue, record):
+    """p.result_layout, remembered per (program, sizes): it is a pure function of them, and a launch-bound call
+    (small N) otherwise spends a large part of its host time recomputing it"""
+    key = (id(p), int(N), int(replay_bytes), int(queue), int(record))
+    hit = _LAYOUTS.get(key)
+    if hit is None or hit[0] is not p:
+        if len(_LAYOUTS) > 4096:
+            _LAYOUTS.clear()
+        hit = (p, p.result_layout(N, replay_bytes, queue, record))   # (p kept alive: its id stays its own)
+        _LAYOUTS[key] = hit
+    return hit[1]
+
+
 def _itemsize(dt):
     return torch.empty((), dtype=dt).element_size()
 
@@ -436,7 +452,7 @@ def run(p, pi, bc, consts=(), target="cuda", ndev=1, stream=None, out=None, rev_
         if tuple(order.shape) != (N,):
             raise TypeError(f"{p.name}: order has shape {tuple(order.shape)}, expected {(N,)}")
     args.append(order)
-    layout, n_zero = p.result_layout(N, replay_bytes, Q, R)
+    layout, n_zero = _layout(p, N, replay_bytes, Q, R)
     res = out if out is not None else alloc_results(p, N, dev, replay_bytes, Q, R)
     if any(t.numel() * t.element_size() < nb for t, (_, nb, _, _) in zip(res, layout)):
         raise ValueError(f"{p.name}: preallocated results are smaller than the launch needs")
@@ -727,7 +743,7 @@ def alloc_results(p, N, device=None, replay_bytes=None, queue=None, record=None,
         replay_bytes = replay_plan(p, max_steps or 2 ** 31 - 1, None, device)[2]
     Q = int(queue or QUEUE_DEFAULT) if p.queue_leaf_bytes else 0
     R = record_capacity(N, record, device, record_slot_bytes(p)) if p.record_bytes else 0
-    layout, n_zero = p.result_layout(N, replay_bytes or 0, Q, R)
+    layout, n_zero = _layout(p, N, replay_bytes or 0, Q, R)
     # the zeroed results (tallies, scratch accumulators, control words, stats) share ONE allocation, each at a
     # 16-byte aligned offset in layout order: Sum tallies of one dtype that follow each other in the layout are then
     # one contiguous range, which the multi-GPU step all_reduces in place with no packing copy
