@@ -609,12 +609,13 @@ def main():
         dom = (fused.kernel, tf_vg, v_ms)
     if sh_vg:
         # the shower's one spawn launch: every particle step draws 4 threefry2x32 (fold_in and three uniforms), every
-        # split 2 more (the children's keys); the steps counted by the launch itself
+        # split 2 more (fold_in of the step key for each of its two children: one per child spawned); the steps and
+        # children counted by the launch itself
         r_last = B.sh_value_and_grad(pi, bc[0], ct[0], max_steps=cfg.max_steps, out=vo)   # (this rank's own counts)
         torch.cuda.synchronize()
         n_steps = int(r_last["steps"][0].item())
         n_spawned = int(r_last["stats"][0].item())
-        dom = (fused.kernel, 4 * n_steps + 2 * n_spawned, v_ms)
+        dom = (fused.kernel, 4 * n_steps + n_spawned, v_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
     tr = TRAFFIC.get(dom[0])
     traffic = None if tr is None else int(round(tr[0] * N))
@@ -624,8 +625,8 @@ def main():
                 f"ncu dram bytes read+write of one launch at N={tr[1]}, scaled by items to N={N}",
                 "peak_source": "measured: tm_probe_threefry at full occupancy on this GPU",
                 "achieved_int32_tops": round(achieved * TF_OPS / 1e3, 3),
-                "work": (f"{dom[1]} threefry2x32 per launch (4 per particle step over {n_steps} steps, 2 per split "
-                         f"over {n_spawned} children; counted by the launch)") if sh_vg else
+                "work": (f"{dom[1]} threefry2x32 per launch (4 per particle step over {n_steps} steps, 1 per child "
+                         f"-- 2 per split -- over {n_spawned} children; counted by the launch)") if sh_vg else
                         (f"{dom[1]} threefry2x32 per launch ({cfg.tf} per forward step, "
                          f"{0 if fused is not None and not fused.replay_state_bytes else cfg.tf_vjp} per step VJP; "
                          "steps from the per-item trip counts and the replay schedule)")} if (cfg.tf or sh_vg) else None
