@@ -32,9 +32,18 @@
 
 namespace tmb {
 
+// A child in the forward and one-pass launches carries its parent's step key kk and its index j (0 or 1) instead of
+// its own key fold_in(kk, j), which it derives at its first step (child_key): the two fold_ins of a split ran in a
+// branch that 41 % of the lanes take, and the warp issued it nearly every step; the one fold_in of a child's first step
+// runs in a branch that 83 % of the lanes take (a shower particle takes ~1.2 steps).  j travels in the sign bit of the
+// child's energy, which is always positive (a particle splits only with E >= 0.5, into fractions z and 1 - z of at
+// least 0.1): the Child keeps its size, and so the shared-memory stacks theirs.  The keys, and so every result,
+// are the same bits.
+__device__ __forceinline__ float child_energy(float E, u32 j) { return j ? -E : E; }
+
 struct ShowerChild {
-  float E, depth;
-  u32 ka, kb;
+  float E, depth;     // (E: the energy, its sign bit the child's index j)
+  u32 ka, kb;         // the parent's step key
 };
 
 struct ShowerState {
@@ -42,7 +51,17 @@ struct ShowerState {
   float E, depth;
   Key key;
   bool alive;
+  i32 kj;             // -1: key is the particle's key; 0 / 1: key is its parent's step key and j this (child_key)
 };
+
+// a child's key at its first step: fold_in(parent step key, j)
+template <class St>
+__device__ __forceinline__ void child_key(St& s) {
+  if (s.kj >= 0) {
+    s.key = fold_in(s.key, (u32)s.kj);
+    s.kj = -1;
+  }
+}
 
 // The loop body above, shared by the forward, the recording forward and the adjoint's replay: travel, the deposit
 // when low (emitted through `emit` unless null), the split decision.  -> the split flag, the energy fraction z of
@@ -106,18 +125,19 @@ struct SHFwd {
   __device__ static void stage(const Params&, unsigned char*) {}
   __device__ static State start(Ctx& c, i64 item) {
     const uint2 kk = __ldg(&c.keys[item]);
-    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true};
+    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true, -1};
   }
   __device__ static State start_child(Ctx&, const Child& ch) {
-    return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true};
+    return State{0, 0, fabsf(ch.E), ch.depth, Key{ch.ka, ch.kb}, true, (i32)(__float_as_uint(ch.E) >> 31)};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
   __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
+    child_key(s);
     const ShowerStepOut o = shower_advance(c.X0, s);
     if (o.low) SumPriv<kNB>::emit(c.sh, c.stats, f2i(s.depth * 8.0f), s.E);
     if (o.split) {
-      const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
-      const Child a{s.E * o.z, s.depth, c0.a, c0.b}, b{s.E * (1.0f - o.z), s.depth, c1.a, c1.b};
+      const Child a{child_energy(s.E * o.z, 0u), s.depth, o.kk.a, o.kk.b};
+      const Child b{child_energy(s.E * (1.0f - o.z), 1u), s.depth, o.kk.a, o.kk.b};
       const bool swap = o.z > 0.5f;          // the lower-energy child (the smaller subtree) runs first
       o0 = swap ? b : a;
       o1 = swap ? a : b;
@@ -162,8 +182,8 @@ struct SHFwd {
 //                  u64[5N + (N + 1) / 2], seq, qctl, ctl, stats | k i32[N], trunc u8[N], ring (E, depth, key, tE,
 //                  root)[Q]
 struct ShowerVGChild {
-  float E, depth;
-  u32 ka, kb;
+  float E, depth;     // (E: the energy, its sign bit the child's index j)
+  u32 ka, kb;         // the parent's step key
   float tE;
   i32 root;
 };
@@ -173,6 +193,7 @@ struct ShowerVGState {
   float E, depth;
   Key key;
   bool alive;
+  i32 kj;             // as ShowerState's
   float tE;
   i32 root;
 };
@@ -255,13 +276,15 @@ struct SHVG1 {
   }
   __device__ static State start(Ctx& c, i64 item) {
     const uint2 kk = __ldg(&c.keys[item]);
-    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true, 1.0f, (i32)item};
+    return State{0, 0, __ldg(&c.E0[item]), __ldg(&c.d0[item]), Key{kk.x, kk.y}, true, -1, 1.0f, (i32)item};
   }
   __device__ static State start_child(Ctx&, const Child& ch) {
-    return State{0, 0, ch.E, ch.depth, Key{ch.ka, ch.kb}, true, ch.tE, ch.root};
+    return State{0, 0, fabsf(ch.E), ch.depth, Key{ch.ka, ch.kb}, true, (i32)(__float_as_uint(ch.E) >> 31), ch.tE,
+                 ch.root};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
   __device__ __forceinline__ static void step(const Ctx& c, State& s, Child& o0, Child& o1, int& n_out) {
+    child_key(s);
     const ShowerStepOut o = shower_advance(c.X0, s);
     c.ns += 1u;
     if (o.low) {
@@ -276,9 +299,8 @@ struct SHVG1 {
       }
     }
     if (o.split) {
-      const Key c0 = fold_in(o.kk, 0u), c1 = fold_in(o.kk, 1u);
-      const Child a{s.E * o.z, s.depth, c0.a, c0.b, s.tE * o.z, s.root};
-      const Child b{s.E * (1.0f - o.z), s.depth, c1.a, c1.b, s.tE * (1.0f - o.z), s.root};
+      const Child a{child_energy(s.E * o.z, 0u), s.depth, o.kk.a, o.kk.b, s.tE * o.z, s.root};
+      const Child b{child_energy(s.E * (1.0f - o.z), 1u), s.depth, o.kk.a, o.kk.b, s.tE * (1.0f - o.z), s.root};
       const bool swap = o.z > 0.5f;          // the lower-energy child (the smaller subtree) runs first
       o0 = swap ? b : a;
       o1 = swap ? a : b;
@@ -547,14 +569,14 @@ struct SHGrad {
       c.last = r.last;
     }
     c.E = E;
-    return State{0, 0, E, d, c.key, true};
+    return State{0, 0, E, d, c.key, true, -1};
   }
   __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.alive; }
   __device__ static void adj_start(const Ctx& c, Adj& a) { a = Adj{0.0f, 0.0f, 0.0f, c.last}; }
   typedef float Stored;   // a stored state is alive with the item's E and key: only depth varies
   __device__ __forceinline__ static Stored store(const State& s) { return s.depth; }
   __device__ __forceinline__ static State restore(const Ctx& c, Stored d, i64 step) {
-    return State{(i32)step, (i32)step, c.E, d, c.key, true};
+    return State{(i32)step, (i32)step, c.E, d, c.key, true, -1};
   }
   __device__ __forceinline__ static void fwd(const Ctx& c, State& s) { shower_advance(c.X0, s); }
   // one recorded child for the spawn being transposed: its initial-state cotangent, after checking that the record
