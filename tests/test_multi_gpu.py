@@ -1,7 +1,7 @@
 """Items sharded over 2 GPUs (one NCCL rank per GPU) against one GPU, as the reference's sharding test
 (tests/sharding.py:112-122): per-item results of each shard bitwise, the exact gradient bitwise (its words are
 all_gathered and combined with carries), float tallies within 1e-4 (the reference's tolerance for a sharded run).
-Skipped with fewer than 2 GPUs."""
+The NCCL tests are skipped with fewer than 2 GPUs; the gloo test runs two ranks on one GPU."""
 import datetime
 import os
 import socket
@@ -130,3 +130,61 @@ def test_two_gpu_fused_value_and_grad_matches_one(cuda):
     for r in res:
         assert np.abs(r[1].astype(np.float64) - hist1).max() <= 1e-4 * np.abs(hist1).max()
         assert r[3].view(np.uint32)[0] == g1.view(np.uint32)[0]
+
+
+def _rank_one_gpu(rank, world, port, n, q):
+    """a rank of the sharded one-pass step on cuda:0, the collectives over gloo (the bench's collective step)"""
+    import torch.distributed as dist
+    from tallymap_b200 import backend as B
+    from tallymap_b200 import parallel
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        x, k = rw_inputs(n)
+        s0, c = parallel.shard(n, rank, world)
+        out = B.run(B.RW_VG1, [x[s0:s0 + c], k[s0:s0 + c]],
+                    [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)], consts=(20000,))
+        res = B.run.last["results"]
+        parallel.all_reduce_sums(out[:2] + [out[3]])
+        gall = torch.zeros(1, device=dev)
+        parallel.combine_exact(res["ct_drift.exact"], 1, gall, out[3])
+        torch.cuda.synchronize()
+        q.put((rank, out[0].cpu().numpy(), out[1].cpu().numpy(), out[4].cpu().numpy(), gall.cpu().numpy(),
+               out[3].cpu().numpy()))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_sharded_one_pass_two_ranks_on_one_gpu(cuda):
+    """the sharded path of the default step with one GPU: two ranks as two processes on cuda:0 (their kernels
+    never wait on each other), each running the one-pass launch on its half of the items, then the collective step
+    over gloo -- all_reduce of the tallies and stats in place, all_gather of the exact gradient words and their
+    combine on the device.  Against one launch over all items: per-item trip counts bitwise, the exact gradient
+    bitwise, the side counts exactly, the histogram within 1e-4 (the reference's sharded-run tolerance,
+    tests/sharding.py:112-122)"""
+    import torch.multiprocessing as mp
+    from tallymap_b200 import backend as B
+    n = 300007
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_rank_one_gpu, args=(r, 2, port, n, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    x, k = rw_inputs(n)
+    one = B.run(B.RW_VG1, [x, k], [np.float32(1.0), np.ones(256, np.float32), np.zeros(2, np.float32)],
+                consts=(20000,))
+    hist1, side1, g1, st1, k1 = (o.cpu().numpy() for o in one[:5])
+    assert np.array_equal(np.concatenate([res[0][3], res[1][3]]), k1)
+    for r in res:
+        assert np.abs(r[1].astype(np.float64) - hist1).max() <= 1e-4 * np.abs(hist1).max()
+        assert np.array_equal(r[2], side1)
+        assert r[4].view(np.uint32)[0] == g1.view(np.uint32)[0]
+        assert np.array_equal(r[5], st1)
