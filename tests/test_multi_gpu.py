@@ -188,3 +188,57 @@ def test_sharded_one_pass_two_ranks_on_one_gpu(cuda):
         assert np.array_equal(r[2], side1)
         assert r[4].view(np.uint32)[0] == g1.view(np.uint32)[0]
         assert np.array_equal(r[5], st1)
+
+
+def _rank_shower_one_gpu(rank, world, port, n, q):
+    import torch.distributed as dist
+    from oracle import oracle as orc
+    from tallymap_b200 import backend as B
+    from tallymap_b200 import parallel
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        E0, d0, keys = orc.sh_inputs(n)
+        s0, c = parallel.shard(n, rank, world)
+        pi = [E0[s0:s0 + c], d0[s0:s0 + c], keys[s0:s0 + c]]
+        ct = np.linspace(-1.0, 1.0, 512).astype(np.float32)
+        r = B.sh_value_and_grad(pi, np.float32(1.0), ct, order=B.energy_order(torch.from_numpy(pi[0]).cuda()))
+        parallel.all_reduce_sums([r["dep"], r["count"], r["stats"]])
+        torch.cuda.synchronize()
+        q.put((rank, r["dep"].cpu().numpy(), r["count"].cpu().numpy(), r["stats"].cpu().numpy(),
+               r["k"].cpu().numpy(), r["g_E"].cpu().numpy()))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_sharded_shower_two_ranks_on_one_gpu(cuda):
+    """the shower's sharded one-pass step (children stay on their rank's GPU; only the forward tallies and stats
+    are reduced) as two gloo ranks on cuda:0, against one launch over all roots: particle count and stats exactly,
+    per-root trip counts and gradients bitwise (exact per-root sums), the deposit within 1e-4"""
+    import torch.multiprocessing as mp
+    from oracle import oracle as orc
+    from tallymap_b200 import backend as B
+    n = 20001
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_rank_shower_one_gpu, args=(r, 2, port, n, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    E0, d0, keys = orc.sh_inputs(n)
+    ct = np.linspace(-1.0, 1.0, 512).astype(np.float32)
+    one = B.sh_value_and_grad([E0, d0, keys], np.float32(1.0), ct)
+    torch.cuda.synchronize()
+    dep1 = one["dep"].cpu().numpy()
+    assert np.array_equal(np.concatenate([res[0][4], res[1][4]]), one["k"].cpu().numpy())
+    assert np.array_equal(np.concatenate([res[0][5], res[1][5]]).view(np.uint32),
+                          one["g_E"].cpu().numpy().view(np.uint32))
+    for r in res:
+        assert np.abs(r[1].astype(np.float64) - dep1).max() <= 1e-4 * np.abs(dep1).max()
+        assert np.array_equal(r[2], one["count"].cpu().numpy()) and np.array_equal(r[3], one["stats"].cpu().numpy())
