@@ -43,6 +43,7 @@ N_ITEMS = 4194304
 MAX_STEPS = 20000
 TF_OPS = 79          # INT32 ops per threefry2x32 (2 XOR + 2 ADD + 20 x (ADD, ROTL, XOR) + 5 x 3 ADD)
 METRIC = "Mitems/s fwd & grad at N=4M, 1/2/4/8 B200, % of roofline vs host CPU"
+WARM_S = 0.25        # seconds of untimed warm-up work at least (the GPU's clock ramps up over the first few ms)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per item of one launch, from the ncu captures summarised
 # under profiles/ (kernel -> (bytes per item, items in the capture)); the bench scales them to its own launch
 TRAFFIC = {
@@ -214,6 +215,14 @@ class Clocks:
             self.rows.append([c.strip() for c in ln.split(",")])
 
     def stop(self):
+        # a timed region shorter than nvidia-smi's start-up and sampling interval (Q1's: well under a millisecond a
+        # step) ends before the first sample: then wait for one, taken right after the region, and say so
+        late = False
+        if self.proc and not self.rows:
+            late = True
+            t_end = time.time() + 3.0
+            while not self.rows and time.time() < t_end and self.proc.poll() is None:
+                time.sleep(0.01)
         if self.proc:
             self.proc.terminate()
             try:
@@ -232,9 +241,12 @@ class Clocks:
         sm = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in mine for n, v in zip(names, r[6:10]) if v.strip().lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(mine[0][3]) if mine[0][3].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(mine)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None,
+               "sm_max_mhz": float(mine[0][3]) if mine[0][3].replace(".", "").isdigit() else None,
+               "reasons": reasons, "samples": len(mine)}
+        if late:
+            out["note"] = "timed region shorter than the sampling interval: sampled right after it"
+        return out
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
@@ -494,11 +506,30 @@ def main():
                                    vo[vnames.index("stats")])
         return out
 
-    for _ in range(args.warmup):
+    def warm():
         fwd()
         grad()
         if fused is not None:
             vg()
+
+    for _ in range(args.warmup):
+        warm()
+    torch.cuda.synchronize()
+    # then more (untimed) warm-up steps, about WARM_S of work: a configuration whose step is well under a millisecond
+    # (Q1) otherwise times its steps while the GPU's clock is still ramping up (0.26 ms a step after 3 warm-up steps,
+    # 0.05 ms after 20).  The count from one more step's time (the first ones include one-time set-up), the same on
+    # every rank (their steps hold collectives).
+    t_w = time.perf_counter()
+    warm()
+    torch.cuda.synchronize()
+    per = time.perf_counter() - t_w
+    extra = max(0, min(10000, int(WARM_S / max(per, 1e-6))))
+    if world > 1:
+        te = torch.tensor([extra], dtype=torch.int64, device=dev)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        extra = int(te.item())
+    for _ in range(extra):
+        warm()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -702,7 +733,7 @@ def main():
     info = _lib.kernel_info(_lib.kernel_id((fused or cfg.grad).kernel)[0])
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mitems/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "clock_warmup_steps": extra, "ms_per_step": round(tot_ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (jax.random algorithm on the host)",
         "config": {"workload": cfg.workload, "items_per_gpu": N, "items_total": N * world,
                    "max_steps": cfg.max_steps, "rev_checkpoints": C_used,
