@@ -134,7 +134,7 @@ FAM = {"rw": "walk1d", "ph": "photon", "q1": "quickstart", "od": "lorenz", "sh":
 OD_FP32_OPS = 255     # f32 add / mul / min / max / abs / compare of one Lorenz RK45 trial step (+ 3 div, 1 sqrt, 1 pow)
 
 
-def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_kernel):
+def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_kernel, v_ms=None, vg_kernel=None):
     """The Lorenz ensemble's roofline: its bound is the issue rate of its own instruction mix (six stage
     evaluations, the error norm, an f32 pow in the shared double-precision math, the accept decision), so the peaks
     are tm_probe_issue's probes of that mix at full occupancy: P0 trial steps/s (kind 2) and P1 (trial step + step
@@ -145,7 +145,8 @@ def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_ke
     checkpoint and fill passes plus one per step VJP, so the forward evaluations alone are micro - steps, of which
     `steps` pair with the VJPs (the probe's kind 3 iteration: a trial step and a step VJP).  Beside it the FP32 pipe:
     the trial steps' algorithmic f32 operations over the forward time against the probe's FP32 instruction rate
-    (kind 1)."""
+    (kind 1).  With the one-pass forward-mode launch timed (v_ms): its peak P2 = (trial step + stage tangents)/s
+    (kind 5), ideal time steps / P2, and it is the headline entry (the step the bench times)."""
     p0, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP, 512, stream, dev)
     p1, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP_VJP, 256, stream, dev)
     pf, _ = _lib.probe_rate(_lib.PROBE_FP32, 8192, stream, dev)
@@ -154,6 +155,19 @@ def od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_ke
     ideal_g = steps / p1 + max(micro - 2 * steps, 0) / p0
     ideal_f = steps / p0
     eq = ideal_g * p0
+    if v_ms is not None:
+        p2, _ = _lib.probe_rate(_lib.PROBE_ODE_STEP_JVP, 256, stream, dev)
+        v_s = v_ms / 1e3
+        r = od_roofline(_lib, stream, dev, steps, micro, f_ms, g_ms, grad_kernel, fwd_kernel)
+        r["modes"]["vg"] = {"kernel": vg_kernel, "achieved": round(steps / v_s / 1e9, 4),
+                            "frac": round(steps / p2 / v_s, 4)}
+        r.update({"kernel": vg_kernel, "achieved": round(steps / v_s / 1e9, 4), "peak": round(p2 / 1e9, 4),
+                  "unit": "G trial steps with tangents/s", "frac": round(steps / p2 / v_s, 4),
+                  "peak_source": "measured: tm_probe_issue kind 5 (the item's trial step with its stages' tangents at "
+                                 "full occupancy, no divergence or memory) on this GPU",
+                  "work": f"{steps} trial steps (accepted + rejected), each with its stages' tangents"})
+        r["probe"]["p2_step_jvp_per_s"] = round(p2, 1)
+        return r
     return {"bound": "issue", "kernel": grad_kernel, "achieved": round(eq / g_s / 1e9, 4), "peak": round(p0 / 1e9, 4),
             "unit": "G trial-step equivalents/s", "frac": round(ideal_g / g_s, 4), "traffic": None,
             "peak_source": "measured: tm_probe_issue kind 2 (the item's trial step at full occupancy, no "
@@ -373,6 +387,7 @@ def oracle_split(cfg, host, n, nth):
     elif cfg.name == "od":
         timed("fwd", lambda: oracle.od_fwd(*h, nthreads=nth, f64acc=False))
         timed("grad", lambda: oracle.od_grad(*h, nthreads=nth))
+        timed("grad_onepass", lambda: oracle.od_vg1(*h, nthreads=nth))
     else:
         timed("fwd", lambda: oracle.sh_fwd(*h, nthreads=nth, f64acc=False))
         timed("grad", lambda: oracle.sh_grad(*h, nthreads=nth))
@@ -663,9 +678,10 @@ def main():
                          "steps from the per-item trip counts and the replay schedule)")} if (cfg.tf or sh_vg) else None
     if cfg.name == "od":
         roofline = od_roofline(_lib, stream, dev, steps_total, replay_micro_steps(kk, C_used), f_ms, g_ms,
-                               cfg.grad.kernel, cfg.fwd.kernel)
+                               cfg.grad.kernel, cfg.fwd.kernel, v_ms if fused is not None else None,
+                               fused.kernel if fused is not None else None)
         tr = TRAFFIC.get(cfg.grad.kernel)
-        if tr is not None:
+        if tr is not None and fused is None:
             # the replay's head buffer: every trial step's state written in the count pass and read in the sweep
             mp = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
             hbm = json.load(open(mp)).get("hbm_gbs") if os.path.exists(mp) else None

@@ -158,6 +158,8 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
  *   kind 3  one trial step and one step VJP of that item per iteration (the replay's sweep mix)
  *   kind 4  one step of the photon-slab item per iteration (its draws, path, voxel, scattering and roulette; the
  *           deposit summed in a register)
+ *   kind 5  one trial step of the Lorenz RK45 item with its stages' tangents per iteration (the one-pass forward-mode
+ *           program's step)
  * (No counterpart in the reference, which reports no rooflines.) */
 int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
                    int64_t* threads_used);

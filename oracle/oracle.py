@@ -73,6 +73,7 @@ def lib():
             L.or_od_fwd.argtypes = [i64, P, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
             L.or_sh_fwd.argtypes = [i64, P, P, P, f32, i32, ctypes.c_int, P, P, P, P, P, ctypes.c_int]
             L.or_od_grad.argtypes = [i64, P, P, P, P, f32, P, P, i32, ctypes.c_int, ctypes.c_int, P, P, P]
+            L.or_od_vg1.argtypes = [i64, P, P, P, P, f32, P, P, i32, ctypes.c_int, P, P, P, P]
             L.or_sh_grad.argtypes = [i64, P, P, P, f32, P, i32, ctypes.c_int, P, P, P, P]
             L.or_sh_vg1.argtypes = [i64, P, P, P, f32, P, i32, ctypes.c_int, P, P]
             _LIB = L
@@ -256,6 +257,23 @@ def od_grad(sigma, rho, y0, item_id, beta=8.0 / 3.0, ct_final=None, ct_mean=1.0,
     lib().or_od_grad(n, _p(sigma), _p(rho), _p(y0), _p(item_id), np.float32(beta), _p(ctf), _p(ctm), max_steps, C,
                      nthreads, _p(g), _p(tr), _p(st))
     return dict(g=g, trunc=tr.astype(bool), stats=st)
+
+
+def od_vg1(sigma, rho, y0, item_id, beta=8.0 / 3.0, ct_final=None, ct_mean=1.0, max_steps=50000, nthreads=0):
+    """forward mode w.r.t. beta in the backend's one-pass order (programs.cpp OdVG1): the exact gradient g f32[1],
+    the trip counts and truncation flags"""
+    sigma, rho = np.ascontiguousarray(sigma, np.float32), np.ascontiguousarray(rho, np.float32)
+    y0, item_id = np.ascontiguousarray(y0, np.float32), np.ascontiguousarray(item_id, np.int32)
+    n = len(sigma)
+    ctf = np.ones(3 * n, np.float32) if ct_final is None else np.ascontiguousarray(ct_final, np.float32).reshape(-1)
+    ctm = np.array([ct_mean], np.float32)
+    g = np.zeros(1, np.float32)
+    k = np.zeros(n, np.int32)
+    tr = np.zeros(n, np.uint8)
+    st = np.zeros(5, np.int32)
+    lib().or_od_vg1(n, _p(sigma), _p(rho), _p(y0), _p(item_id), np.float32(beta), _p(ctf), _p(ctm), max_steps,
+                    nthreads, _p(g), _p(k), _p(tr), _p(st))
+    return dict(g=g, k=k, trunc=tr.astype(bool), stats=st)
 
 
 def sh_inputs(n, seed=5):

@@ -585,6 +585,77 @@ struct OdGrad : OdBase {
   void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
 };
 
+// Forward mode w.r.t. beta, the checker of the backend's one-pass Lorenz program (items_ode.cuh ODVG1, its order, not
+// the reference's): each item carries the tangents dy, dk1 of y and k1 (dy = 0 and dk1 = f_jvp(y0, 0) before the
+// loop); a step's stage tangents are dz = dy + hh * (sum a_j dk_j) in the primal's order and dk = f_jvp(z, dz), beta's
+// tangent 1, hh and the step control without tangents (the step factor is stop_gradient'ed); an accepted step takes
+// dy5 and dk7.  An item adds ((ct_f0 dy_x + ct_f1 dy_y) + ct_f2 dy_z) + ct_mean (dy_z / 2^20) to an exact bin.
+struct OdVG1 : OdBase {
+  const float *ctf, *ctm;
+  i32* k_out;
+  uint8_t* trunc;
+  i32* stats;
+  ExactBins* gbins;
+  struct Priv { ExactBins b{1}; };
+  static void f_jvp(float sg, float rh, float bt, const float* y, const float* dy, float* o) {
+    o[0] = sg * (dy[1] - dy[0]);
+    o[1] = (dy[0] * (rh - y[2]) + y[0] * (-dy[2])) - dy[1];
+    o[2] = (dy[0] * y[1] + y[0] * dy[1]) - (y[2] + bt * dy[2]);
+  }
+  void item(i64 i, Priv& p) const {
+    const float sg = sigma[i], rh = rho[i];
+    OdState s = start(i);
+    float dy[3] = {0.0f, 0.0f, 0.0f}, dk1[3];
+    f_jvp(sg, rh, beta, s.y, dy, dk1);
+    while (cond(s)) {
+      const float hh = std::fmin(s.h, 10.0f - s.tt);
+      St st;
+      stages(sg, rh, beta, s.y, s.k1, hh, st);
+      float dK[6][3], dz[3], dy5[3], dk7[3];
+      for (int c = 0; c < 3; ++c) dK[0][c] = dk1[c];
+      for (int q = 1; q <= 5; ++q) {
+        for (int c = 0; c < 3; ++c) {
+          float d = kDP.a[q - 1][0] * dK[0][c];
+          for (int j = 1; j < q; ++j) d = d + kDP.a[q - 1][j] * dK[j][c];
+          dz[c] = dy[c] + hh * d;
+        }
+        f_jvp(sg, rh, beta, st.Z[q], dz, dK[q]);
+      }
+      for (int c = 0; c < 3; ++c) {
+        float d = kDP.b[0] * dK[0][c];
+        for (int j = 2; j < 6; ++j) d = d + kDP.b[j] * dK[j][c];
+        dy5[c] = dy[c] + hh * d;
+      }
+      f_jvp(sg, rh, beta, st.Y5, dy5, dk7);
+      float fac;
+      if (control(s.y, st, hh, &fac)) {
+        s.tt = s.tt + hh;
+        for (int c = 0; c < 3; ++c) {
+          s.y[c] = st.Y5[c];
+          s.k1[c] = st.K[6][c];
+          dy[c] = dy5[c];
+          dk1[c] = dk7[c];
+        }
+      }
+      s.h = hh * fac;
+      s.kc += 1;
+      s.k += 1;
+    }
+    const i32 iid = id[i];
+    float gi = 0.0f;
+    for (int c = 0; c < 3; ++c) {
+      if (iid < 0 || (i64)iid * 3 + c >= nbins) continue;
+      const float t = ctf[(i64)iid * 3 + c] * dy[c];
+      gi = c == 0 ? t : gi + t;
+    }
+    gi = gi + ctm[0] * (dy[2] * (1.0f / 1048576.0f));
+    exact_emit_priv(p.b, 0, gi, stats);
+    trunc[i] = (s.kc >= M && s.tt < 10.0f) ? 1 : 0;
+    k_out[i] = s.k;
+  }
+  void flush(Priv& p) const { exact_flush(p.b, *gbins, 1, stats); }
+};
+
 // ================================================================================================= SH: shower
 // The item of benchmark configuration 5 (jax-style source in tallymap_b200/csrc/items_shower.cuh, restated here).  The
 // reference runs spawned children through a shared ticket ring on its OpenMP team (kernel.py:778-811, 1007-1044);
@@ -889,6 +960,18 @@ int or_od_grad(i64 n, const float* sigma, const float* rho, const float* y0, con
   OdGrad p;
   p.sigma = sigma; p.rho = rho; p.y0 = y0; p.id = id; p.beta = beta; p.M = max_steps; p.nbins = 3 * n;
   p.ctf = ctf; p.ctm = ctm; p.C = C; p.trunc = trunc; p.stats = stats; p.gbins = &gb;
+  team_run(p, n, nthreads);
+  exact_readout(gb, 1, g, stats);
+  return 0;
+}
+
+int or_od_vg1(i64 n, const float* sigma, const float* rho, const float* y0, const i32* id, float beta,
+              const float* ctf, const float* ctm, i32 max_steps, int nthreads, float* g, i32* k_out, uint8_t* trunc,
+              i32* stats) {
+  ExactBins gb(1);
+  OdVG1 p;
+  p.sigma = sigma; p.rho = rho; p.y0 = y0; p.id = id; p.beta = beta; p.M = max_steps; p.nbins = 3 * n;
+  p.ctf = ctf; p.ctm = ctm; p.k_out = k_out; p.trunc = trunc; p.stats = stats; p.gbins = &gb;
   team_run(p, n, nthreads);
   exact_readout(gb, 1, g, stats);
   return 0;

@@ -129,7 +129,7 @@ EXPORTS = ("tm_abi_version", "tm_last_error", "tm_kernel_id", "tm_kernel_name", 
            "tm_compile_register", "tm_compile")
 
 
-PROBE_THREEFRY, PROBE_FP32, PROBE_ODE_STEP, PROBE_ODE_STEP_VJP, PROBE_PHOTON_STEP = 0, 1, 2, 3, 4
+PROBE_THREEFRY, PROBE_FP32, PROBE_ODE_STEP, PROBE_ODE_STEP_VJP, PROBE_PHOTON_STEP, PROBE_ODE_STEP_JVP = 0, 1, 2, 3, 4, 5
 
 
 def probe_rate(kind, iters, stream, device, reps=3):

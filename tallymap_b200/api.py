@@ -117,7 +117,8 @@ FAMILIES = {
                      {(0,): B.RW_VG1}),
     "photon": Family("photon", B.PH_FWD, {(0, 1): B.PH_GRAD}, (0, None, None), 100000, {}, {(0, 1): B.PH_VG1},
                      onepass_grad=True),
-    "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000),
+    "lorenz": Family("lorenz", B.OD_FWD, {(0,): B.OD_GRAD}, (0, 0, 0, 0, None), 50000, {}, {(0,): B.OD_VG1},
+                     onepass_grad=True),
     # reverse mode through spawn: the tree adjoint (backend.tree_grad), w.r.t. X0 and the roots' E and depth
     # (roots claimed largest energy first: a root's subtree grows with its energy, so the launch's tail is small trees)
     "shower": Family("shower", B.SH_FWD, {"tree": B.tree_grad}, (0, 0, 0, None), 100000, onepass_grad=True,

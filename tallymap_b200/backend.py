@@ -244,6 +244,10 @@ OD_GRAD = ItemProgram("od_grad", "od_grad", pi=OD_PI,
                       consts=("max_steps", "rev_checkpoints", "replay_threads", "bins3"),
                       tallies=(TSpec("ct_beta", (1,), exact=True),),
                       ys=(Operand("truncated", (), torch.uint8),), trunc=0, replay_state_bytes=32)
+# the Lorenz ensemble's value and grad w.r.t. beta in one forward pass by forward mode (the tangents of y and k1
+# carried with the state; csrc/items_ode.cuh ODVG1): within the float tolerance of the replay's gradient
+OD_VG1 = ItemProgram("od_vg_onepass", "od_vg_onepass", pi=OD_PI, bc=OD_GRAD.bc, consts=("max_steps", "bins3"),
+                     tallies=OD_FWD.tallies + OD_GRAD.tallies, ys=OD_FWD.ys, trunc=1)
 
 # benchmark configuration 5, the branching shower (csrc/items_shower.cuh): a spawning program with a ring of Q slots
 SH_FWD = ItemProgram("sh_fwd", "sh_fwd", pi=(Operand("E", (), _F32), Operand("depth", (), _F32), KEY),

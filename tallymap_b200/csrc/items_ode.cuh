@@ -160,6 +160,36 @@ struct OdeCommon {
   // returns s = hh * ct_z, which each a_j then scales into ct_kj
   __device__ __forceinline__ static V3 stage_vjp(const P& p, const V3& z, const V3& kz, float hh, float& dsum,
                                                  V3& cy);
+  // the tangent of f at y along dy, beta's tangent 1 (jax's jvp rules of f's expressions, term by term)
+  __device__ __forceinline__ static V3 f_jvp(const P& p, const V3& y, const V3& dy) {
+    return V3{p.sigma * (dy.y - dy.x), (dy.x * (p.rho - y.z) + y.x * (-dy.z)) - dy.y,
+              (dy.x * y.y + y.x * dy.y) - (y.z + p.beta * dy.z)};
+  }
+  // the tangents of the stages (s: the primal stages at the same state): each stage point's tangent
+  // dz = dy + hh * (sum a_j dk_j) in the primal's order (hh and the step control carry no tangent: the step factor
+  // is stop_gradient'ed), each stage's dk = f_jvp(z, dz); -> dy5, dk7 in *dy5, *dk7
+  __device__ __forceinline__ static void stages_jvp(const P& p, const V3& dy, const V3& dk1, float hh,
+                                                    const Stages& s, V3* dy5, V3* dk7) {
+    const V3 dk2 = f_jvp(p, s.z2, axpy(dy, hh, V3{DP::a21 * dk1.x, DP::a21 * dk1.y, DP::a21 * dk1.z}));
+    const V3 dk3 = f_jvp(p, s.z3, axpy(dy, hh, V3{DP::a31 * dk1.x + DP::a32 * dk2.x, DP::a31 * dk1.y + DP::a32 * dk2.y,
+                                                   DP::a31 * dk1.z + DP::a32 * dk2.z}));
+    const V3 dk4 = f_jvp(p, s.z4, axpy(dy, hh, V3{DP::a41 * dk1.x + DP::a42 * dk2.x + DP::a43 * dk3.x,
+                                                   DP::a41 * dk1.y + DP::a42 * dk2.y + DP::a43 * dk3.y,
+                                                   DP::a41 * dk1.z + DP::a42 * dk2.z + DP::a43 * dk3.z}));
+    const V3 dk5 = f_jvp(p, s.z5, axpy(dy, hh, V3{DP::a51 * dk1.x + DP::a52 * dk2.x + DP::a53 * dk3.x + DP::a54 * dk4.x,
+                                                   DP::a51 * dk1.y + DP::a52 * dk2.y + DP::a53 * dk3.y + DP::a54 * dk4.y,
+                                                   DP::a51 * dk1.z + DP::a52 * dk2.z + DP::a53 * dk3.z + DP::a54 * dk4.z}));
+    const V3 dk6 = f_jvp(p, s.z6, axpy(dy, hh, V3{DP::a61 * dk1.x + DP::a62 * dk2.x + DP::a63 * dk3.x +
+                                                       DP::a64 * dk4.x + DP::a65 * dk5.x,
+                                                   DP::a61 * dk1.y + DP::a62 * dk2.y + DP::a63 * dk3.y +
+                                                       DP::a64 * dk4.y + DP::a65 * dk5.y,
+                                                   DP::a61 * dk1.z + DP::a62 * dk2.z + DP::a63 * dk3.z +
+                                                       DP::a64 * dk4.z + DP::a65 * dk5.z}));
+    *dy5 = axpy(dy, hh, V3{DP::b1 * dk1.x + DP::b3 * dk3.x + DP::b4 * dk4.x + DP::b5 * dk5.x + DP::b6 * dk6.x,
+                           DP::b1 * dk1.y + DP::b3 * dk3.y + DP::b4 * dk4.y + DP::b5 * dk5.y + DP::b6 * dk6.y,
+                           DP::b1 * dk1.z + DP::b3 * dk3.z + DP::b4 * dk4.z + DP::b5 * dk5.z + DP::b6 * dk6.z});
+    *dk7 = f_jvp(p, s.y5, *dy5);
+  }
   // the VJP of f at y for cotangent g: ct_y (returned) and the beta term (*db)
   __device__ __forceinline__ static V3 f_vjp(const P& p, const V3& y, const V3& g, float* db) {
     *db = -(y.z * g.z);
@@ -363,6 +393,126 @@ struct ODGrad : OdeCommon {
   }
 };
 
+// ------------------------------------------------------------------------------------ one pass: forward mode
+// The forward's outputs and the gradient w.r.t. beta of <ct_final, final> + ct_mean * mean_z in ONE forward launch:
+// each item carries the tangents dy, dk1 of its active carries y, k1 w.r.t. beta (the pre-loop k1 = f(y0) starts
+// them at dy = 0, dk1 = f_jvp(y0, 0)); a step computes the stages' tangents beside the stages (stages_jvp) and an
+// accepted step takes dy5, dk7; at the end the item's contribution ((ct_f0 dy_x + ct_f1 dy_y) + ct_f2 dy_z) +
+// ct_mean (dy_z / 2^20) (0 for a dropped final bin) is one f32 value added to an exact bin, so the gradient does not
+// depend on which thread ran which item.  No scratch and no replay: the same derivative as the replay adjoint, its
+// terms summed in another order -- within the float tolerance, not bitwise; bitwise the oracle's od_vg1, which
+// restates this order.
+//   od_vg_onepass  sigma, rho, y0, item_id, beta, ct_final f32[N*3], ct_mean f32[1], consts (max_steps, 3N), order |
+//                  final f32[N*3], mean_z f32[1], g f32[1], exact u64[6], ctl, stats | k i32[N], trunc u8[N]
+struct OdeVGState {
+  i32 kc, k;
+  float tt, h;
+  V3 y, k1, dy, dk1;
+};
+
+struct ODVG1 : OdeCommon {
+  static constexpr int kMinBlocks = 6;
+  enum { kSigma, kRho, kY0, kId, kBeta, kCtFinal, kCtMean, kConsts, kOrder, kFinal, kMean, kG, kExact, kCtl, kStats,
+         kK, kTrunc, kNBuf };
+  enum { kConstM, kConstBins };
+  static constexpr int kMeanOff = ExactBins<1>::kSmemBytes;          // mean_z privatised after the exact words
+  static constexpr int kSmemBytes = kMeanOff + 16;
+  struct Ctx {
+    const float *sigma, *rho, *y0;
+    const i32* id;
+    P p;
+    i32 M;
+    i64 n_final;
+    const float *ctf;
+    float ctm;
+    float *fin, *mean, *sh, *g;
+    u64* gw;
+    i32* stats;
+    i32* kout;
+    uint8_t* trunc;
+    mutable ExactPrivS<1> pv;
+  };
+  typedef OdeVGState State;
+  __device__ static void setup(Ctx& c, const Params& P_, unsigned char* smem) {
+    c.sigma = static_cast<const float*>(P_.p[kSigma]);
+    c.rho = static_cast<const float*>(P_.p[kRho]);
+    c.y0 = static_cast<const float*>(P_.p[kY0]);
+    c.id = static_cast<const i32*>(P_.p[kId]);
+    c.p.beta = __ldg(static_cast<const float*>(P_.p[kBeta]));
+    c.M = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstM);
+    c.n_final = __ldg(static_cast<const i32*>(P_.p[kConsts]) + kConstBins);
+    c.ctf = static_cast<const float*>(P_.p[kCtFinal]);
+    c.ctm = __ldg(static_cast<const float*>(P_.p[kCtMean]));
+    c.fin = static_cast<float*>(P_.p[kFinal]);
+    c.mean = static_cast<float*>(P_.p[kMean]);
+    c.sh = reinterpret_cast<float*>(smem + kMeanOff);
+    c.g = static_cast<float*>(P_.p[kG]);
+    c.gw = static_cast<u64*>(P_.p[kExact]);
+    c.stats = static_cast<i32*>(P_.p[kStats]);
+    c.kout = static_cast<i32*>(P_.p[kK]);
+    c.trunc = static_cast<uint8_t*>(P_.p[kTrunc]);
+    c.pv.bind(smem + ExactBins<1>::kPrivOffset);
+  }
+  __device__ static void stage(const Params&, unsigned char*) {}
+  __device__ static State start(Ctx& c, i64 item) {
+    c.p.sigma = __ldg(&c.sigma[item]);
+    c.p.rho = __ldg(&c.rho[item]);
+    const V3 y{__ldg(&c.y0[3 * item]), __ldg(&c.y0[3 * item + 1]), __ldg(&c.y0[3 * item + 2])};
+    const V3 z{0.0f, 0.0f, 0.0f};
+    return State{0, 0, 0.0f, 1e-3f, y, f(c.p, y), z, f_jvp(c.p, y, z)};
+  }
+  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) { return s.kc < c.M && s.tt < kT1; }
+  __device__ __forceinline__ static void step(const Ctx& c, State& st) {
+    const float hh = fminf(st.h, kT1 - st.tt);
+    Stages s;
+    stages(c.p, st.y, st.k1, hh, s);
+    V3 dy5, dk7;
+    stages_jvp(c.p, st.dy, st.dk1, hh, s, &dy5, &dk7);
+    float fac;
+    const bool ok = control(st.y, st.k1, s, hh, &fac);
+    if (ok) {
+      st.tt = st.tt + hh;
+      st.y = s.y5;
+      st.k1 = s.k7;
+      st.dy = dy5;
+      st.dk1 = dk7;
+    }
+    st.h = hh * fac;
+    st.kc += 1;
+    st.k += 1;
+  }
+  __device__ static void finish(const Ctx& c, const State& s, i64 item) {
+    const i32 iid = __ldg(&c.id[item]);
+    const float v[3] = {s.y.x, s.y.y, s.y.z};
+    const float dv[3] = {s.dy.x, s.dy.y, s.dy.z};
+    float gi = 0.0f;
+    for (int j = 0; j < 3; ++j) {
+      if (iid < 0 || (i64)iid * 3 + j >= c.n_final) {
+        atomicAdd(&c.stats[kStDroppedEmits], 1);
+      } else {
+        fatom(&c.fin[(i64)iid * 3 + j], v[j]);
+        const float t = __ldg(&c.ctf[(i64)iid * 3 + j]) * dv[j];
+        gi = j == 0 ? t : gi + t;
+      }
+    }
+    gi = gi + c.ctm * (s.dy.z * kInvN);
+    fatom(c.sh, s.y.z * kInvN);
+    if (c.pv.emit(0, gi)) atomicAdd(&c.stats[kStFixedPointOverflow], 1);
+    c.kout[item] = s.k;
+    c.trunc[item] = (s.kc >= c.M && s.tt < kT1) ? 1 : 0;
+  }
+  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int) {
+    ExactBins<1>::flush(c.pv, const_cast<unsigned char*>(smem), c.gw, c.stats, tid);
+    if (tid == 0) {
+      const float v = *reinterpret_cast<const float*>(smem + kMeanOff);
+      if (v != 0.0f) fatom(c.mean, v);
+    }
+  }
+  __device__ static void epilogue(const Ctx& c, int tid, int) {
+    if (tid == 0) ExactBins<1>::readout(c.gw, c.g, c.stats);
+  }
+};
+
 }  // namespace tmb
 
 namespace tmb {
@@ -371,7 +521,8 @@ namespace tmb {
 // taking the same path, no claims, no emits, no memory traffic besides one word per thread at the end.
 //   kVjp == 0: one trial step per iteration (advance: the six stages, the error norm, pow, the accept decision);
 //   kVjp == 1: a trial step and the step VJP at the state before it (the replay's sweep: stages recomputed, then
-//             run backwards), per iteration.
+//             run backwards), per iteration;
+//   kVjp == 2: a trial step with the stages' tangents (the one-pass forward-mode step, ODVG1::step), per iteration.
 // Each thread integrates its own Lorenz system (sigma, rho and y0 vary slightly by thread, as the ensemble's);
 // the integration window is restarted when it ends, so every iteration is a full trial step.  Each variant is its own
 // kernel, so each gets the register allocation, and so the occupancy, of its own code.  The rate at full occupancy is the issue-rate speed of light of the item's own instruction mix: the roofline's peak for the
@@ -386,6 +537,20 @@ __global__ void __launch_bounds__(TM_BLOCK) probe_ode_kernel(u32 iters, u32* out
   ODGrad::Adj a;
   ODGrad::adj_start(c, a);
   a.cy = V3{1.0f, 0.5f, 0.25f};
+  if (kVjp == 2) {
+    ODVG1::Ctx cv;
+    cv.p = c.p;
+    cv.M = 0x7fffffff;
+    const V3 z{0.0f, 0.0f, 0.0f};
+    OdeVGState sv{0, 0, 0.0f, 1e-3f, y0, OdeCommon::f(c.p, y0), z, OdeCommon::f_jvp(c.p, y0, z)};
+    for (u32 i = 0; i < iters; ++i) {
+      ODVG1::step(cv, sv);
+      if (!(sv.tt < OdeCommon::kT1)) sv = OdeVGState{sv.kc, sv.k, 0.0f, 1e-3f, sv.y, sv.k1, z, sv.dk1};
+    }
+    out[t] = __float_as_uint(sv.y.x) ^ __float_as_uint(sv.h) ^ (u32)sv.k ^ __float_as_uint(sv.dy.x) ^
+             __float_as_uint(sv.dk1.z);
+    return;
+  }
   for (u32 i = 0; i < iters; ++i) {
     if (kVjp) {
       const OdeState at = st;

@@ -134,6 +134,7 @@ void init_registry() {
   add_forward<tmb::PHVG1>("ph_vg_onepass");
   add_forward<tmb::ODFwd>("od_fwd");
   add_replay<tmb::ODGrad, 1>("od_grad");
+  add_forward<tmb::ODVG1>("od_vg_onepass");
   add_spawn<tmb::SHFwd>("sh_fwd");
   add_spawn<tmb::SHRec>("sh_rec");
   add_spawn<tmb::SHVG1>("sh_vg_onepass");
@@ -572,12 +573,13 @@ int tm_probe_threefry(void* stream, int32_t iters, uint32_t* out, int64_t out_le
 
 int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int64_t out_len,
                    int64_t* threads_used) {
-  if (!out || iters < 1 || out_len < 128 || kind < 0 || kind > 4)
+  if (!out || iters < 1 || out_len < 128 || kind < 0 || kind > 5)
     return fail(TM_EINVAL, "tallymap_b200: tm_probe_issue: bad arguments");
   const void* fn = kind == 0 ? (const void*)tmb::probe_threefry_kernel
                  : kind == 1 ? (const void*)tmb::probe_fp32_kernel
                  : kind == 2 ? (const void*)tmb::probe_ode_kernel<0>
-                 : kind == 3 ? (const void*)tmb::probe_ode_kernel<1> : (const void*)tmb::probe_photon_kernel;
+                 : kind == 3 ? (const void*)tmb::probe_ode_kernel<1>
+                 : kind == 5 ? (const void*)tmb::probe_ode_kernel<2> : (const void*)tmb::probe_photon_kernel;
   int dev = 0, sms = 0, occ = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
@@ -591,6 +593,7 @@ int tm_probe_issue(void* stream, int32_t kind, int32_t iters, uint32_t* out, int
   else if (kind == 1) tmb::probe_fp32_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   else if (kind == 2) tmb::probe_ode_kernel<0><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   else if (kind == 3) tmb::probe_ode_kernel<1><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
+  else if (kind == 5) tmb::probe_ode_kernel<2><<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   else tmb::probe_photon_kernel<<<(unsigned)blocks, 128, 0, st>>>((tmb::u32)iters, out);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("probe kernel", e);
   if (threads_used) *threads_used = blocks * 128;

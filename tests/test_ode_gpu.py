@@ -83,3 +83,68 @@ def test_od_full_size(cuda, orc):
     lm = fm["final"].astype(np.float64).sum() + float(fm["mean"][0])
     fd = (lp - lm) / (float(BETA + h) - float(BETA - h))
     assert np.isfinite(g["g"]).all() and abs(float(g["g"][0]) - fd) <= 0.05 * abs(fd)
+
+
+# ---------------------------------------------------------------------------------------------- one pass
+def gpu_od_vg(inp, beta=BETA, ctf=None, ctm=1.0, M=50000):
+    n = len(inp[0])
+    ctf = np.ones((n, 3), np.float32) if ctf is None else ctf
+    out = B.run(B.OD_VG1, list(inp), [beta, ctf, np.float32(ctm)], consts=(M,))
+    torch.cuda.synchronize()
+    B.check_status(B.run.last["ctl"])
+    fin, mean, g, stats, k, tr = [o.cpu().numpy() for o in out]
+    return dict(final=fin, mean=mean.reshape(1), g=g, stats=stats, k=k, trunc=tr.astype(bool))
+
+
+@pytest.mark.parametrize("n", [1, 4000, 65536 + 5])
+def test_od_vg_onepass(cuda, orc, n):
+    """forward mode w.r.t. beta in one launch: the gradient bitwise the oracle's forward mode (the same order), within
+    the float tolerance of the replay adjoint; trip counts, flags, stats and the final states bitwise the forward's"""
+    inp = orc.od_inputs(n, seed=11)
+    ctf = np.random.default_rng(2).normal(size=(n, 3)).astype(np.float32)
+    got = gpu_od_vg(inp, ctf=ctf, ctm=0.5)
+    ref = orc.od_vg1(*inp, ct_final=ctf, ct_mean=0.5)
+    assert np.array_equal(got["g"].view(np.uint32), ref["g"].view(np.uint32))
+    fw = orc.od_fwd(*inp)
+    assert np.array_equal(got["k"], fw["k"]) and np.array_equal(got["trunc"], fw["trunc"])
+    assert np.array_equal(got["stats"], fw["stats"])
+    assert np.array_equal(got["final"].view(np.uint32), fw["final"].view(np.uint32))
+    assert abs(float(got["mean"][0]) - float(fw["mean"][0])) <= 1e-5 * abs(float(fw["mean"][0]))
+    rp = orc.od_grad(*inp, ct_final=ctf, ct_mean=0.5)
+    assert abs(float(got["g"][0]) - float(rp["g"][0])) <= 1e-4 * max(abs(float(rp["g"][0])), 1e-6)
+
+
+def test_od_vg_onepass_truncation_and_ids(cuda, orc):
+    """dropped final bins contribute nothing (and are counted); max_steps = 50 truncates items: the flags and the
+    gradient of what ran, bitwise the oracle's"""
+    sigma, rho, y0, ids = orc.od_inputs(2000, seed=5)
+    ids = ids.copy()
+    ids[::7] = -1
+    ids[3] = 2000
+    inp = (sigma, rho, y0, ids)
+    for M in (50, 50000):
+        got = gpu_od_vg(inp, M=M)
+        ref = orc.od_vg1(*inp, max_steps=M)
+        assert np.array_equal(got["g"].view(np.uint32), ref["g"].view(np.uint32))
+        assert np.array_equal(got["trunc"], ref["trunc"]) and np.array_equal(got["k"], ref["k"])
+        assert got["stats"][4] > 0
+
+
+def test_od_api_value_and_grad_onepass(cuda, orc):
+    """value_and_grad of the Lorenz ensemble runs the one-pass launch (exact_order=True: the forward and the replay);
+    a truncated item poisons both gradients"""
+    import tallymap_b200 as tm
+    inp = orc.od_inputs(3000, seed=7)
+    f = tm.vmap("lorenz", outputs={"final": tm.Sum((3000, 3)), "mean_z": tm.Sum(())}, in_axes=(0, 0, 0, 0, None))
+    cts = {"final": torch.ones(3000, 3), "mean_z": torch.tensor(0.25)}
+    r1, g1 = f.value_and_grad(*inp, BETA, wrt=4, cotangents=cts)
+    assert B.run.last["kernel"] == "od_vg_onepass"
+    r2, g2 = f.value_and_grad(*inp, BETA, wrt=4, cotangents=cts, exact_order=True)
+    torch.cuda.synchronize()
+    assert abs(float(g1) - float(g2)) <= 1e-4 * abs(float(g2))
+    assert torch.equal(r1.outputs["final"], r2.outputs["final"]) and torch.equal(r1.per_item, r2.per_item)
+    ft = tm.vmap("lorenz", outputs={"final": tm.Sum((3000, 3)), "mean_z": tm.Sum(())}, in_axes=(0, 0, 0, 0, None),
+                 max_steps=50)
+    _, gt = ft.value_and_grad(*inp, BETA, wrt=4, cotangents=cts)
+    torch.cuda.synchronize()
+    assert torch.isnan(gt)
