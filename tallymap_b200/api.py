@@ -232,8 +232,8 @@ class Mapped:
         them): ONE replay launch (for the shower: the tree adjoint).  cotangents: {output name: array of the output's
         shape}; missing outputs get zero cotangents.  -> a scalar for one index, a vector for a tuple; NaN when an
         item's replay hit max_steps.  exact_order=False: where the family's one-pass program is forward mode (the
-        photon, the Lorenz ensemble, the shower), that launch instead, its forward outputs discarded -- faster than the replay, which
-        re-runs the forward, and equal to it within the float tolerance."""
+        photon, the Lorenz ensemble, the shower), that launch instead, its forward outputs discarded -- faster than
+        the replay, which re-runs the forward, and equal to it within the float tolerance."""
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
         if not exact_order and self.fam.onepass_grad:
             return self.value_and_grad(*args, wrt=wrt, cotangents=cotangents)[1]
