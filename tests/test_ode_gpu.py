@@ -83,6 +83,11 @@ def test_od_full_size(cuda, orc):
     lm = fm["final"].astype(np.float64).sum() + float(fm["mean"][0])
     fd = (lp - lm) / (float(BETA + h) - float(BETA - h))
     assert np.isfinite(g["g"]).all() and abs(float(g["g"][0]) - fd) <= 0.05 * abs(fd)
+    # the one-pass forward mode (the bench's step) at full size: the replay's gradient within 1e-4, the forward's
+    # trip counts and final states bitwise
+    v = gpu_od_vg(inp)
+    assert abs(float(v["g"][0]) - float(g["g"][0])) <= 1e-4 * abs(float(g["g"][0]))
+    assert np.array_equal(v["k"], a["k"]) and np.array_equal(v["final"].view(np.uint32), a["final"].view(np.uint32))
 
 
 # ---------------------------------------------------------------------------------------------- one pass
