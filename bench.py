@@ -55,6 +55,7 @@ TRAFFIC = {
     "ph_fwd": ((10.557440e6 + 0.0) / 1048576, 1048576),
     "od_grad": ((3.060892e9 + 3.133417e9) / 262144, 262144),
     "od_fwd": ((0.009466e9 + 0.0) / 262144, 262144),
+    "od_vg_onepass": ((12634368 + 0) / 262144, 262144),
 }
 
 
@@ -680,14 +681,15 @@ def main():
         roofline = od_roofline(_lib, stream, dev, steps_total, replay_micro_steps(kk, C_used), f_ms, g_ms,
                                cfg.grad.kernel, cfg.fwd.kernel, v_ms if fused is not None else None,
                                fused.kernel if fused is not None else None)
-        tr = TRAFFIC.get(cfg.grad.kernel)
-        if tr is not None and fused is None:
-            # the replay's head buffer: every trial step's state written in the count pass and read in the sweep
+        # (the replay: its head buffer, every trial step's state written in the count pass and read in the sweep; the
+        # one-pass launch: the inputs once)
+        tr = TRAFFIC.get(fused.kernel if fused is not None else cfg.grad.kernel)
+        if tr is not None:
             mp = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
             hbm = json.load(open(mp)).get("hbm_gbs") if os.path.exists(mp) else None
             roofline["traffic"] = int(round(tr[0] * N))
             roofline["traffic_source"] = f"ncu dram bytes read+write of one launch at N={tr[1]}, scaled by items to N={N}"
-            gbs = roofline["traffic"] / (g_ms / 1e3) / 1e9
+            gbs = roofline["traffic"] / ((v_ms if fused is not None else g_ms) / 1e3) / 1e9
             roofline["hbm"] = {"achieved": round(gbs, 2), "unit": "GB/s", "peak": hbm,
                                "frac": round(gbs / hbm, 4) if hbm else None,
                                "peak_source": "measured: MEASURED_PEAKS.json hbm_gbs" if hbm else None}
