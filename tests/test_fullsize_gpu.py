@@ -89,7 +89,8 @@ def test_ph_full_size_against_oracle(cuda, orc):
 
 def test_od_full_size_against_oracle(cuda, orc):
     """benchmark configuration 4, N = 1,048,576 Lorenz systems: every item's final state (each bin of Sum((N, 3)) is
-    written once, so exact), the accepted + rejected step counts, and the replay gradient w.r.t. beta"""
+    written once, so exact), the accepted + rejected step counts, the replay gradient w.r.t. beta and the one-pass
+    forward-mode gradient"""
     n, M = 1048576, 50000
     inp = orc.od_inputs(n)
     beta = np.float32(8.0 / 3.0)
@@ -104,6 +105,12 @@ def test_od_full_size_against_oracle(cuda, orc):
     assert abs(float(mean.reshape(-1)[0]) - float(ref["mean"][0])) <= FT * abs(float(ref["mean"][0]))
     rep = orc.od_grad(*inp, beta=beta, ct_final=ctf, ct_mean=0.5, max_steps=M, C=4096)
     assert np.array_equal(bits(g), bits(rep["g"])) and np.array_equal(g_tr.astype(bool), rep["trunc"])
+    # the one-pass forward-mode launch (the bench's step): bitwise the oracle's forward mode at full size
+    fin1, mean1, g1, st1, k1, tr1 = run(B.OD_VG1, list(inp), [beta, ctf, np.float32(0.5)], M)
+    ref1 = orc.od_vg1(*inp, beta=beta, ct_final=ctf, ct_mean=0.5, max_steps=M)
+    assert np.array_equal(bits(g1), bits(ref1["g"])) and np.array_equal(k1, ref["k"])
+    assert np.array_equal(bits(fin1.reshape(n, 3)), bits(ref["final"])) and np.array_equal(st1, ref["stats"])
+    assert abs(float(g1[0]) - float(g[0])) <= 1e-4 * abs(float(g[0]))
 
 
 def test_sh_full_size_against_oracle(cuda, orc):

@@ -153,3 +153,10 @@ def test_od_api_value_and_grad_onepass(cuda, orc):
     _, gt = ft.value_and_grad(*inp, BETA, wrt=4, cotangents=cts)
     torch.cuda.synchronize()
     assert torch.isnan(gt)
+
+
+def test_od_vg_onepass_empty(cuda):
+    """no items: no kernel runs; zero outputs and a zero gradient"""
+    inp = (np.zeros(0, np.float32), np.zeros(0, np.float32), np.zeros((0, 3), np.float32), np.zeros(0, np.int32))
+    got = gpu_od_vg(inp, ctf=np.zeros((0, 3), np.float32))
+    assert got["final"].size == 0 and got["k"].size == 0 and float(got["g"][0]) == 0.0 and got["stats"].sum() == 0
