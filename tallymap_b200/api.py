@@ -524,7 +524,10 @@ class MappedFn:
         adjoint.  A broadcast operand's cotangent is summed over the items (exactly); a per-item operand's is per
         item (shape (N,) or (N, n)).  -> one cotangent for one index, a tuple in `wrt`'s order for a tuple (for
         broadcast operands only: a vector, as before); NaN when an item's replay hit max_steps.  A spawning item:
-        reverse mode through spawn, the recording forward and one launch per generation (_tree)."""
+        reverse mode through spawn, the recording forward and one launch per generation (_tree).  Records outputs:
+        cotangents[name] = {float field: f32[capacity]} in the canonical layout; a forward launch gives the adjoint
+        each item's record count and offset first; NaN when a Records output overflowed its capacity or a replay
+        appended a different number of records."""
         L = self.lowered(args)
         if L.it.spawns:
             if order is not None or n_active is not None:
@@ -539,16 +542,33 @@ class MappedFn:
         pi, bc = self._split(args)
         n = int((pi[0] if isinstance(pi[0], torch.Tensor) else B._host(pi[0])).shape[0]) if pi else 0
         cts = []
-        for name, (shape, dt, _) in self.outputs.items():
-            if dt != "f32":
+        for name, o in self.outputs.items():
+            if o[0] == "records" or o[1] != "f32":
                 continue
             c = cotangents.get(name)
-            cts.append(torch.zeros(shape, dtype=torch.float32) if c is None else c)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+        over = False
+        if L.fwd.records:
+            # (a Records output's cotangents sit at its canonical slots: the adjoint needs each item's record count
+            # and offset, so a forward launch runs first -- the reference's fill twin reads the primal's counts)
+            fout = B.run(L.fwd, pi, bc, consts=(self.max_steps,), n_active=n_active)
+            fys = fout[len(L.fwd.tallies) + 1:]
+            pi = list(pi)
+            for r, (nm, cap, fields) in enumerate(L.fwd.records):
+                cnt = fys[L.n_results + r]
+                pi += [cnt, torch.cumsum(cnt.to(torch.int64), 0) - cnt.to(torch.int64)]
+                over = over | (cnt.to(torch.int64).sum() > cap)
+            for nm, cap, fields in L.fwd.records:
+                given = cotangents.get(nm) or {}
+                for f, dt in fields:
+                    if dt == torch.float32:
+                        c = given.get(f)
+                        cts.append(torch.zeros(cap, dtype=torch.float32) if c is None else c)
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order,
                     rev_checkpoints=self.opts["rev_checkpoints"], n_active=n_active)
         ct = out[0].reshape(-1)
         ys = out[2:]
-        bad = ys[prog.trunc].bool().any()
+        bad = ys[prog.trunc].bool().any() | over
         nan = lambda v: torch.where(bad, torch.full_like(v, float("nan")), v)
         if not pidx:
             return self._per_arg(nan(ct), where, wrt, idx)
@@ -561,7 +581,8 @@ class MappedFn:
         wrt: float32 broadcast argument index or tuple of indices, W scalars in all (a broadcast vector counts its n
         elements, in order); tangents: W values (one tangent lane) or an
         array [L, W] (L <= 16 lanes, the reference's dual lanes).  -> (Result, {output name: tangent}), a tangent of
-        shape (*output.shape) for one lane, (L, *output.shape) for L lanes; NaN when an item hit max_steps."""
+        shape (*output.shape) for one lane, (L, *output.shape) for L lanes; a Records output's tangent is {float
+        field: its tangent in the canonical layout, (capacity,) or (L, capacity)}; NaN when an item hit max_steps."""
         from . import lower
         L_ = self.lowered(args)
         idx = (wrt,) if isinstance(wrt, int) else tuple(wrt)
@@ -579,6 +600,7 @@ class MappedFn:
         pi, bc = self._split(args)
         out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,),
                     queue=self.spawn.capacity if self.spawn else None, n_active=n_active)
+        raw = B.run.last["results"]
         nf = len(L_.fwd.tallies)
         nt = len(prog.tallies)
         tallies = {t.name: v for t, v in zip(prog.tallies[:nf], out[:nf])}
@@ -591,10 +613,30 @@ class MappedFn:
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
         bad = _limits(prog, stats)
-        res = Result(_poison(tallies, bad), self._per_item(L_, per[:L_.n_results]), trunc, stats)
+        rec_out, rec_t = {}, {}
+        if prog.records:
+            # the records and their fields' tangents in the canonical layout (moved together, _records.py canon);
+            # a Records output past its capacity poisons every float output and tangent, as in the forward
+            counts = {nm: ys[L_.n_results + r] for r, (nm, _, _) in enumerate(prog.records)}
+            recs = B.canonical_records(prog, raw, counts)
+            stats["appended"] = {nm: tot for nm, (_, tot) in recs.items()}
+            stats["records_dropped"] = {nm: torch.clamp(tot - cap, min=0)
+                                        for (nm, cap, _), (_, tot) in zip(prog.records, recs.values())}
+            if any(int(v) > 0 for v in stats["records_dropped"].values()):
+                bad = bad | True
+            for nm, cap, fields in L_.fwd.records:
+                rec = recs[nm][0]
+                rec_out[nm] = {f: rec[f] for f, _ in fields}
+                rec_t[nm] = {f: torch.stack([rec[f"{f}#d{l}"] for l in range(L)]) for f, dt in fields
+                             if dt == torch.float32}
+        outs = _poison(tallies, bad)
+        for nm, rec in rec_out.items():
+            outs[nm] = rec if not bool(n_tr > 0) else _poison(rec, n_tr > 0)
+        res = Result(outs, self._per_item(L_, per[:L_.n_results]), trunc, stats)
         dts = _poison(dts, bad)
+        dts.update({nm: _poison(t, bad) for nm, t in rec_t.items()})
         if not lanes_given:
-            dts = {k: v[0] for k, v in dts.items()}
+            dts = {k: ({f: t[0] for f, t in v.items()} if isinstance(v, dict) else v[0]) for k, v in dts.items()}
         return res, dts
 
     def jacfwd(self, *args, wrt):

@@ -891,10 +891,11 @@ class _Rev:
     """reverse-mode code for a straight-line equation list: cotangent locals, first contribution assigned, later ones
     added (jax's add_jaxvals order)"""
 
-    def __init__(self, active, indent="    ", tag="g", spawn_t=None):
+    def __init__(self, active, indent="    ", tag="g", spawn_t=None, append_t=None):
         self.active, self.ct, self.lines, self.indent, self.tag = active, {}, [], indent, tag
         self.n = 0
         self.spawn_t = spawn_t      # the transpose of a spawn (the tree adjoint), else spawns have no cotangent
+        self.append_t = append_t    # the transpose of a Records append, else appends have no cotangent
 
     def add(self, x, expr):
         if not isinstance(x, T.Var) or x.id not in self.active:
@@ -913,6 +914,10 @@ class _Rev:
             if e.prim == "spawn":
                 if self.spawn_t is not None:
                     self.spawn_t(self, e, names)
+                continue
+            if e.prim == "append":
+                if self.append_t is not None:
+                    self.append_t(self, e, names)
                 continue
             if e.prim == "emit":
                 idx, v = e.ins
@@ -1018,9 +1023,17 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     cotangents of the child's initial state, which the next-deeper generation's launch wrote to dx[slot]; the
     item's children are consumed newest first along the recorded chain, and each must hold exactly the leaves the
     replay spawns (else tree[0] counts a mismatch: _reverse_spawn.py:22-26).  At the end a child writes its own
-    initial state's cotangents to dx[own slot], a root to the per-item results (every float per-item operand)."""
+    initial state's cotangents to dx[own slot], a root to the per-item results (every float per-item operand).
+    Records outputs (tallymap/_records.py twin): per output r, the forward's per-item record counts and canonical
+    offsets (the exclusive prefix sum of the counts) are per-item operands after the item's own, and each float
+    field's cotangent f32[capacity] a broadcast operand after the tallies' cotangents.  An append's transpose (the
+    item's appends consumed newest first) gives its float fields the cotangents at canonical slot offset + k, k its
+    ordinal; a replay whose append count differs from the forward's flags the item as truncated, which poisons the
+    gradient."""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
+    recs = list(tr.records.items()) if not tree else []
+    rindex = {rname: r for r, (rname, _) in enumerate(recs)}
     if tree:
         wrt_pi = _float_operands(it)
     Lw = len(it.loads)
@@ -1043,10 +1056,17 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     enum = []
     for j in range(npi):
         enum.append(f"kIn{j} = {idx}"); idx += 1
+    for r in range(len(recs)):
+        enum.append(f"kRCnt{r} = {idx}"); idx += 1
+        enum.append(f"kROff{r} = {idx}"); idx += 1
     for k in range(nbc):
         enum.append(f"kBc{k} = {idx}"); idx += 1
     for q, (t, name, shape) in enumerate(ftal):
         enum.append(f"kCt{q} = {idx}"); idx += 1
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f, (fname, dt) in enumerate(fields):
+            if dt == T.F32:
+                enum.append(f"kRCt{r}F{f} = {idx}"); idx += 1
     # (the tree adjoint's control words come first among its outputs: a later generation's launch zeroes them
     # alone, while the exact words sum over every launch)
     names_ = ("kRecord", "kRootLast", "kConsts", "kOrder", "kCtl", "kG", "kExact", "kStats", "kTree") if tree else \
@@ -1096,6 +1116,10 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     if tree:
         ctx += ["    const i32* rec;", "    const i32* root_last;", "    float* dx;", "    u32* tree;", "    bool roots;",
                 "    i64 R;", "    i32 last;   // the current item's newest child"]
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        ctx += [f"    const i32* rcnt{r};", f"    const long long* roff{r};",
+                f"    i32 rn{r};   // the current item's records in the forward", f"    long long ro{r};"]
+        ctx += [f"    const float* rct{r}f{f};" for f, (fname, dt) in enumerate(fields) if dt == T.F32]
     ctx.append("  };")
     lines += ctx
     if standalone:
@@ -1127,6 +1151,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("    bool has_post;")
     if tree:
         lines.append("    i32 cur;   // the next recorded child to consume, newest first")
+    for r in range(len(recs)):
+        lines.append(f"    i32 ka{r};   // output {r}'s appends not yet transposed")
     lines.append("  };")
     # setup / stage
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -1138,6 +1164,11 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines += ["    c.stats = static_cast<i32*>(P.p[kStats]);", "    c.gw = static_cast<u64*>(P.p[kExact]);",
               "    c.g = static_cast<float*>(P.p[kG]);", "    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);"]
     lines += [f"    c.gpi{q} = static_cast<float*>(P.p[kGpi{q}]);" for q in range(len(pl))]
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        lines += [f"    c.rcnt{r} = static_cast<const i32*>(P.p[kRCnt{r}]);",
+                  f"    c.roff{r} = static_cast<const long long*>(P.p[kROff{r}]);"]
+        lines += [f"    c.rct{r}f{f} = static_cast<const float*>(P.p[kRCt{r}F{f}]);"
+                  for f, (fname, dt) in enumerate(fields) if dt == T.F32]
     if tree:
         lines += ["    c.rec = static_cast<const i32*>(P.p[kRecord]);",
                   "    c.root_last = static_cast<const i32*>(P.p[kRootLast]);",
@@ -1164,6 +1195,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     else:
         for v, ld in it.loads:
             lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
+    for r in range(len(recs)):
+        lines += [f"    c.rn{r} = __ldg(&c.rcnt{r}[item]);", f"    c.ro{r} = __ldg(&c.roff{r}[item]);"]
     lines += _emit_code(tr.pre, names, None, skip_emits=True)
     for i in it.saved:
         lines.append(f"    c.p{i} = {names[i]};")
@@ -1175,7 +1208,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  __device__ __forceinline__ static bool cond(const Ctx& c, const State& s) {")
     lines.append("    return s.kc < c.M && pred(c, s);")
     lines.append("  }")
-    lines.append(f"  __device__ static void adj_start(const Ctx&{' c' if tree else ''}, Adj& a) {{")
+    lines.append(f"  __device__ static void adj_start(const Ctx&{' c' if tree or recs else ''}, Adj& a) {{")
     for j, a_ in enumerate(carry_act):
         if a_:
             lines.append(f"    a.cc{j} = 0.0f;")
@@ -1187,6 +1220,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("    a.has_post = false;")
     if tree:
         lines.append("    a.cur = c.last;")
+    for r in range(len(recs)):
+        lines.append(f"    a.ka{r} = c.rn{r};")
     lines.append("  }")
     lines.append("  __device__ __forceinline__ static Stored store(const State& s) {")
     lines.append("    Stored o;")
@@ -1207,6 +1242,30 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  }")
     bc_pos = {it.bc[k].id: q for q, k in enumerate(wrt)}
     nsp = [0]
+    nap = [0]
+
+    def append_t(rev, e, names):
+        """a Records append's transpose: its float fields' cotangents from the canonical slot offset + k"""
+        nap[0] += 1
+        k = nap[0]
+        r = rindex[e.params["records"]]
+        cap, fields = tr.records[e.params["records"]]
+        when = _ref(e.ins[0], names)
+        took = [(f, x) for f, ((fname, dt), x) in enumerate(zip(fields, e.ins[1:]))
+                if dt == T.F32 and isinstance(x, T.Var) and x.id in rev.active]
+        ind = rev.indent
+        out = [f"{ind}float ra{k}_{f} = 0.0f;" for f, _ in took]
+        out.append(f"{ind}if ({when}) {{")
+        out.append(f"{ind}  a.ka{r} -= 1;")
+        if took:
+            out.append(f"{ind}  const long long s_ = c.ro{r} + (long long)a.ka{r};")
+            out.append(f"{ind}  if (a.ka{r} >= 0 && s_ < {int(cap)}ll) {{")
+            out += [f"{ind}    ra{k}_{f} = __ldg(&c.rct{r}f{f}[s_]);" for f, _ in took]
+            out.append(f"{ind}  }}")
+        out.append(f"{ind}}}")
+        rev.lines += out
+        for f, x in took:
+            rev.add(x, f"ra{k}_{f}")
 
     def spawn_t(rev, e, names):
         """a spawn's transpose: the recorded child's initial-state cotangents into the spawned leaves"""
@@ -1256,7 +1315,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {")
     names = _names_loop(it, tr.carry, "at")
     lines += _emit_code(tr.body, names, None, skip_emits=True)
-    rev = _Rev(act, spawn_t=spawn_t if tree else None)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None)
     for j, x in enumerate(tr.body_out):
         if carry_act[j]:
             rev.add(x, f"a.cc{j}")
@@ -1268,7 +1327,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  __device__ static void post_vjp(const Ctx& c, const State& fin, Adj& a) {")
     names = _names_loop(it, tr.post_carry, "fin")
     lines += _emit_code(tr.post, names, None, skip_emits=True)
-    rev = _Rev(act, spawn_t=spawn_t if tree else None)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None)
     rev.run(tr.post, names, ct_tally)
     lines += rev.lines
     lines += finish_rev(rev, tr.post_carry, True, "pb")
@@ -1312,7 +1371,9 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
         # the per-item operand's cotangent: what the pre-loop VJP gathered into its leaves (+0 for an unused one)
         for e_, v in enumerate(leaves):
             lines.append(f"    c.gpi{q}[item * {len(leaves)} + {e_}] = {rev.ct.get(v.id, '0.0f')};")
-    lines.append("    c.trunc[item] = (fin.kc >= c.M && pred(c, fin)) ? 1 : 0;")
+    # (a replay whose appends differ in number from the forward's is flagged: its records' cotangents were misread)
+    miss = "".join(f" || a.ka{r} != 0" for r in range(len(recs)))
+    lines.append(f"    c.trunc[item] = ((fin.kc >= c.M && pred(c, fin)){miss}) ? 1 : 0;")
     lines.append("  }")
     lines.append("  __device__ static void adj_flush(const Ctx& c, unsigned char* smem, int tid, int) {")
     lines.append(f"    ExactBins<{Wx}>::flush(c.pv, smem, c.gw, c.stats, tid);")
@@ -1461,8 +1522,6 @@ class Lowered:
             for k in wrt:
                 if self.bc[k].dtype != torch.float32:
                     raise LowerError("tallymap_b200.lower: only float32 broadcast operands have tangents")
-            if self.fwd.records:
-                raise NotImplementedError("tallymap_b200: forward mode of Records outputs is not lowered")
             src, smem = jvp_source(self.it, list(wrt), int(lanes))
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             bc = self.bc + (Operand("tangents", (int(lanes), len(wrt)), torch.float32),)
@@ -1471,12 +1530,18 @@ class Lowered:
                                                for nm, shape in fts)
             sp = self.it.spawns
             nx = sum(1 for t in tallies if t.exact)
-            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + 2 + len(self.fwd.ys) + (3 if sp else 0)
+            # a Records output's float fields gain one tangent field per lane ("field#d<lane>"), after the fields
+            records = tuple((nm, cap, fields + tuple((f"{f}#d{l}", torch.float32) for f, dt in fields
+                                                     if dt == torch.float32 for l in range(int(lanes))))
+                            for nm, cap, fields in self.fwd.records)
+            nrec = sum(len(fl) + 3 for _, _, fl in records)
+            nbuf = len(self.pi) + len(bc) + 2 + len(tallies) + nx + nrec + 2 + len(self.fwd.ys) + (3 if sp else 0)
             kid = self._compile(src, f"{self.name}_jvp{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
             self.jvps[key] = ItemProgram(f"{self.name}_jvp", kid, pi=self.pi, bc=bc,
                                          consts=("max_steps", "queue") if sp else ("max_steps",),
                                          tallies=tallies, ys=self.fwd.ys, trunc=self.fwd.trunc, spawns=sp,
-                                         queue_leaf_bytes=self._child_bytes(int(lanes)) if sp else 0)
+                                         queue_leaf_bytes=self._child_bytes(int(lanes)) if sp else 0,
+                                         records=records)
         return self.jvps[key]
 
     def _child_bytes(self, L):
@@ -1580,8 +1645,6 @@ class Lowered:
         self._differentiable(wrt)
         from .backend import ItemProgram, TSpec
         wrt, wrt_pi = tuple(wrt), tuple(wrt_pi)
-        if self.fwd.records:
-            raise NotImplementedError("tallymap_b200: reverse mode of an item with Records outputs is not lowered")
         if self.it.spawns:
             raise ValueError("tallymap_b200: a spawning item's reverse mode is the tree adjoint (rec_program, "
                              "tree_program)")
@@ -1594,12 +1657,17 @@ class Lowered:
             fts = [(nm, shape) for nm, (shape, dt) in self.it.specs if dt == T.F32]
             from .backend import Operand
             bc = self.bc + tuple(Operand("ct_" + nm, tuple(shape), torch.float32) for nm, shape in fts)
+            # Records outputs: the forward's per-item counts and canonical offsets, and the float fields' cotangents
+            pi = self.pi + tuple(o for nm, _, _ in self.fwd.records
+                                 for o in (Operand(f"{nm}#count", (), torch.int32), Operand(f"{nm}#offset", (), torch.int64)))
+            bc += tuple(Operand(f"ct_{nm}.{f}", (cap,), torch.float32) for nm, cap, fields in self.fwd.records
+                        for f, dt in fields if dt == torch.float32)
             ys = tuple(Operand(f"ct_in{j}", self.pi[j].shape, torch.float32) for j in wrt_pi)
             ys += (_operand("truncated", T.BOOL),)
-            nbuf = len(self.pi) + len(bc) + 2 + 4 + len(ys) + 1
+            nbuf = len(pi) + len(bc) + 2 + 4 + len(ys) + 1
             tag = "".join(map(str, wrt)) + ("_pi" + "".join(map(str, wrt_pi)) if wrt_pi else "")
             kid = self._compile(src, f"{self.name}_grad{tag}", nbuf, smem)
-            self.grads[key] = ItemProgram(f"{self.name}_grad", kid, pi=self.pi, bc=bc,
+            self.grads[key] = ItemProgram(f"{self.name}_grad", kid, pi=pi, bc=bc,
                                           consts=("max_steps", "rev_checkpoints", "replay_threads"),
                                           tallies=(TSpec("ct", (max(len(wrt), 1),), exact=True),),
                                           ys=ys, trunc=len(ys) - 1,
@@ -1677,9 +1745,10 @@ def _jvp_rule(e, a, d, out):
     raise LowerError(f"tallymap_b200.lower: no jvp rule for {p}")
 
 
-def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    ", spawner=None):
+def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    ", spawner=None, appender=None):
     """straight-line primal code with each active value's L tangents; tnames: id -> [L tangent expressions];
-    spawner(when, leaves, leaf tangents): a spawn with its children's tangents"""
+    spawner(when, leaves, leaf tangents): a spawn with its children's tangents; appender(records, when, fields,
+    field tangents): a Records append with its float fields' tangents"""
     out = []
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
@@ -1687,6 +1756,11 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
             if spawner is not None:
                 tl = [tnames.get(x.id) if isinstance(x, T.Var) else None for x in e.ins[1:]]
                 out.append(indent + spawner(a[0], a[1:], tl))
+            continue
+        if e.prim == "append":
+            if appender is not None:
+                tl = [tnames.get(x.id) if isinstance(x, T.Var) else None for x in e.ins[1:]]
+                out.append(indent + appender(e.params["records"], a[0], a[1:], tl))
             continue
         out += _emit_code([e], names, emitter, indent)
         if e.prim == "emit":
@@ -1726,6 +1800,11 @@ def jvp_source(it, wrt, L, contract=False):
     if not 1 <= L <= LANES_MAX:
         raise LowerError(f"tallymap_b200.lower: 1..{LANES_MAX} tangent lanes")
     sp = it.spawns
+    # Records outputs (forward mode proper only): each append writes its float fields' L tangents beside the fields,
+    # at the same raw slot, so the canonical layout moves them with their records (tallymap/_records.py canon)
+    recs = list(tr.records.items())         # [(name, (capacity, ((field, dtype), ...)))]
+    if recs and contract:
+        raise LowerError("tallymap_b200.lower: Records outputs have no one-pass forward-mode value-and-grad")
     # a spawning item: a child carries its float per-item inputs' tangents (fl: their positions among the leaves)
     fl = [m for m, (v, _) in enumerate(it.loads) if v.dtype == T.F32] if sp else []
     act, carry_act = _active(it, wrt, extra=[it.loads[m][0].id for m in fl])
@@ -1761,6 +1840,16 @@ def jvp_source(it, wrt, L, contract=False):
             enum.append(f"kX{t} = {idx}"); idx += 1
         for t, _ in ex:
             enum.append(f"kDX{t} = {idx}"); idx += 1
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f in range(len(fields)):
+            enum.append(f"kR{r}F{f} = {idx}"); idx += 1
+        for f, (fname, dt) in enumerate(fields):
+            if dt == T.F32:
+                for l in range(L):
+                    enum.append(f"kR{r}D{f}_{l} = {idx}"); idx += 1
+        enum.append(f"kR{r}Cid = {idx}"); idx += 1
+        enum.append(f"kR{r}K = {idx}"); idx += 1
+        enum.append(f"kR{r}Ctr = {idx}"); idx += 1
     if sp:
         enum.append(f"kSeq = {idx}"); idx += 1
         enum.append(f"kQctl = {idx}"); idx += 1
@@ -1768,6 +1857,8 @@ def jvp_source(it, wrt, L, contract=False):
     enum.append(f"kStats = {idx}"); idx += 1
     for r in range(len(tr.results)):
         enum.append(f"kY{r} = {idx}"); idx += 1
+    for r in range(len(recs)):
+        enum.append(f"kR{r}N = {idx}"); idx += 1
     enum.append(f"kTrunc = {idx}"); idx += 1
     if sp:
         enum.append(f"kQueue = {idx}"); idx += 1
@@ -1844,6 +1935,14 @@ def jvp_source(it, wrt, L, contract=False):
     for i in act_saved:
         for l in range(L):
             ctx.append(f"    float dp{i}_{l};")
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f, (fname, dt) in enumerate(fields):
+            ctx.append(f"    {CTYPE[dt]}* r{r}f{f};")
+            if dt == T.F32:
+                ctx += [f"    float* r{r}d{f}_{l};" for l in range(L)]
+        ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;", f"    i32* r{r}n;"]
+    if recs:
+        ctx.append("    i64 item;")
     ctx.append("  };")
     lines += ctx
     lines.append("  struct State {")
@@ -1856,6 +1955,8 @@ def jvp_source(it, wrt, L, contract=False):
     if contract:
         for l in range(L):
             lines.append(f"    float a{l};   // the item's cotangent of bc[{wrt[l]}] so far")
+    for r in range(len(recs)):
+        lines.append(f"    i32 rc{r};   // records appended by the item so far")
     lines.append("  };")
     tidx = {name: t for t, (name, _) in enumerate(it.specs)}
     lines.append("  __device__ static void setup(Ctx& c, const Params& P, unsigned char* smem) {")
@@ -1899,6 +2000,14 @@ def jvp_source(it, wrt, L, contract=False):
                   f"    c.pv.bind(smem + ExactBins<{W}>::kPrivOffset);"]
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
+    for r, (rname, (cap, fields)) in enumerate(recs):
+        for f, (fname, dt) in enumerate(fields):
+            lines.append(f"    c.r{r}f{f} = static_cast<{CTYPE[dt]}*>(P.p[kR{r}F{f}]);")
+            if dt == T.F32:
+                lines += [f"    c.r{r}d{f}_{l} = static_cast<float*>(P.p[kR{r}D{f}_{l}]);" for l in range(L)]
+        lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);", f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
+                  f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);",
+                  f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);"]
     lines.append("  }")
     if contract:
         lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
@@ -1942,6 +2051,25 @@ def jvp_source(it, wrt, L, contract=False):
         return f"{{ const i32 b_ = {idx_c}; if ((u32)b_ < {S}u) fatom(&{tgt}[{l * S} + b_], {dv_c}); }}"
 
     bc_t = {it.bc[k].id: [f"c.db{k}_{l}" for l in range(L)] for k in wrt}
+    rindex = {rname: r for r, (rname, _) in enumerate(recs)}
+
+    def appender_for(counter):
+        def appender(rname, when_c, vals_c, vals_t):
+            """one record at the next raw slot (as the forward's), its float fields' tangents beside it; -0.0 is
+            stored as +0.0 (its tangent unchanged)"""
+            r = rindex[rname]
+            cap, fields = tr.records[rname]
+            st = [f"if ({when_c}) {{ const unsigned long long o_ = atomicAdd(c.r{r}ctr, 1ull); "
+                  f"if (o_ < {int(cap)}ull) {{"]
+            for f, ((fname, dt), v) in enumerate(zip(fields, vals_c)):
+                st.append(f" c.r{r}f{f}[o_] = {v}{' + 0.0f' if dt == T.F32 else ''};")
+                if dt == T.F32:
+                    for l in range(L):
+                        tv = vals_t[f][l] if vals_t[f] is not None else "0.0f"
+                        st.append(f" c.r{r}d{f}_{l}[o_] = {tv};")
+            st.append(f" c.r{r}cid[o_] = (i32)c.item; c.r{r}k[o_] = {counter(r)}; }} {counter(r)} += 1; }}")
+            return "".join(st)
+        return appender
 
     def spawner(when_c, leaves_c, leaf_t):
         """a child's leaves and, for its float leaves, their tangents"""
@@ -1975,6 +2103,9 @@ def jvp_source(it, wrt, L, contract=False):
             for l in range(L):
                 lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
         lines += ["    State s;", "    s.kc = 0;"]
+        if recs:
+            lines.append("    c.item = item;")
+            lines += [f"    s.rc{r} = 0;" for r in range(len(recs))]
         if contract:
             for l in range(L):
                 lines.append(f"    s.a{l} = a{l};")
@@ -2006,7 +2137,8 @@ def jvp_source(it, wrt, L, contract=False):
     names = _names_loop(it, tr.carry)
     tn = loop_tn(tr.carry, "s")
     acc["p"] = "s.a"
-    lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter, spawner=spawner)
+    lines += _emit_code_jvp(tr.body, names, tn, act, L, emitter, temitter, spawner=spawner,
+                            appender=appender_for(lambda r: f"s.rc{r}"))
     for j, x in enumerate(tr.body_out):
         lines.append(f"    const {CTYPE[tr.carry[j].dtype]} n{j} = {_ref(x, names)};")
         if carry_act[j]:
@@ -2032,7 +2164,10 @@ def jvp_source(it, wrt, L, contract=False):
         acc["p"] = "a"
         for l in range(L):
             lines.append(f"    float a{l} = s.a{l};")
-    lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter, spawner=spawner)
+    for r in range(len(recs)):
+        lines.append(f"    i32 rc{r} = s.rc{r};")
+    lines += _emit_code_jvp(tr.post, names, tn, act, L, emitter, temitter, spawner=spawner,
+                            appender=appender_for(lambda r: f"rc{r}"))
     if contract:
         for l in range(L):
             lines.append(f"    if (c.pv.emit({l}, a{l})) atomicAdd(&c.stats[kStFixedPointOverflow], 1);")
@@ -2042,6 +2177,8 @@ def jvp_source(it, wrt, L, contract=False):
         lines.append("    if (child) { if (tr_) atomicAdd(&c.stats[kStChildrenTruncated], 1); return; }")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r}[item] = {_ref(y, names)};")
+    for r in range(len(recs)):
+        lines.append(f"    c.r{r}n[item] = rc{r};")
     lines.append("    c.trunc[item] = " + ("tr_ ? 1 : 0;" if sp else "(s.kc >= c.M && pred(c, s)) ? 1 : 0;"))
     lines.append("  }")
     lines.append("  __device__ static void flush(const Ctx& c, const unsigned char* smem, int tid, int nth) {")

@@ -352,3 +352,18 @@ def drift2d(t, x0, key, a):
     k, x, t = tl.while_loop(lambda c: inside(c[1]), body, (0, x0, t))
     t = t.add("exits", (x[0] > 1.0).astype(tl.int32) + 2 * (x[1] > 1.0).astype(tl.int32), 1.0)
     return t, x, k
+
+
+def decay_records(t, w, key, a):
+    """six steps per item; a step records (step, a * weight) when its draw is below 0.6, and the item's final
+    (weight, steps): every recorded value is a polynomial in the broadcast a, the number of records is not a
+    function of a (Records outputs under forward and reverse mode)"""
+    def body(c):
+        k, w, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.append("hits", {"k": k, "w": w * a}, when=u < 0.6)
+        t = t.add("tot", 0, w)
+        return k + 1, w * (0.5 + 0.4 * u) * a, t
+    k, w, t = tl.while_loop(lambda c: c[0] < 6, body, (0, w, t))
+    t = t.append("last", {"k": k, "w": w})
+    return t, k

@@ -107,8 +107,13 @@ def test_records_lower_and_compile():
     names = [n for n, _, _, _ in L.fwd.result_layout(16)[0]]
     assert names[:3] == ["hist", "hits.k", "hits.x"] and "exit#ctr" in names and "hits#count" in names
     assert "atomicAdd(c.r0ctr, 1ull)" in L.fwd_source
-    with pytest.raises(NotImplementedError):
-        L.grad_program((0,))
+    # reverse mode: the forward's per-item counts and offsets become per-item operands, the float fields'
+    # cotangents broadcast operands; forward mode: a tangent field per float field and lane
+    g = L.grad_program((0,))
+    assert [o.name for o in g.pi] == ["in0", "in1", "hits#count", "hits#offset", "exit#count", "exit#offset"]
+    assert [o.name for o in g.bc] == ["bc0", "ct_hist", "ct_hits.x"]
+    j = L.jvp_program((0,), 2)
+    assert [f for f, _ in dict((nm, fl) for nm, _, fl in j.records)["hits"]] == ["k", "x", "x#d0", "x#d1"]
 
 
 def test_ir_evaluator_matches_the_oracle(orc):

@@ -1,0 +1,116 @@
+"""Records outputs under forward and reverse mode (the reference's fill twin, tallymap/_records.py:1-19): the jvp
+writes each record's float-field tangents beside it and the canonical layout moves them with it; the replay adjoint
+reads a record's field cotangents at its canonical slot (the forward's per-item counts and offsets).  Checked
+against central differences of the IR evaluator's canonical records, against each other (<ct, J t> both ways),
+and for the poisoning of an overflowed output."""
+import numpy as np
+import pytest
+import torch
+
+import tallymap_b200 as tm
+from tallymap_b200 import backend as B
+from tallymap_b200 import prng
+
+pytestmark = pytest.mark.gpu
+CAP = 1 << 14
+
+
+def _setup(n=2000, cap=CAP):
+    from items_lang import decay_records
+    rng = np.random.default_rng(21)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(23), n)
+    outs = {"tot": tm.Sum(()), "hits": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=cap),
+            "last": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=n)}
+    f = tm.vmap(decay_records, outputs=outs, in_axes=(0, 0, None), max_steps=64)
+    return f, w, keys
+
+
+def _records(w, keys, a, n):
+    """the IR evaluator's canonical records (item order, append order) of decay_records: hits w, last w"""
+    from items_lang import decay_records
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    tr = T.trace_item(decay_records, ["f32", "key", "f32"], 2, {"tot": ((), "f32")},
+                      {"hits": (CAP, (("k", "i32"), ("w", "f32"))), "last": (n, (("k", "i32"), ("w", "f32")))})
+    r = Evaluator(tr, 64).run([w, keys], [np.float32(a)])
+    hw = np.array([rec[1] for rec in r["records"]["hits"]], np.float64)
+    lw = np.array([rec[1] for rec in r["records"]["last"]], np.float64)
+    return hw, lw, float(r["sums"]["tot"][0])
+
+
+def test_records_jvp_against_central_difference(cuda):
+    f, w, keys = _setup()
+    a, h = 1.05, 1e-3
+    r, d = f.jvp(w, keys, np.float32(a), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    m = int(r.stats["appended"]["hits"])
+    assert 0 < m < CAP and int(r.stats["appended"]["last"]) == len(w)
+    hp, lp, tp = _records(w, keys, a + h, len(w))
+    hm, lm, tm_ = _records(w, keys, a - h, len(w))
+    h0, l0, _ = _records(w, keys, a, len(w))
+    assert len(hp) == len(hm) == len(h0) == m
+    dh, dl = d["hits"]["w"].cpu().numpy().astype(np.float64), d["last"]["w"].cpu().numpy().astype(np.float64)
+    assert np.allclose(dh[:m], (hp - hm) / (2 * h), rtol=1e-3, atol=1e-4) and not dh[m:].any()
+    assert np.allclose(dl, (lp - lm) / (2 * h), rtol=1e-3, atol=1e-4)
+    # the primal records in the canonical layout, bitwise the forward's
+    r0 = f(w, keys, np.float32(a))
+    torch.cuda.synchronize()
+    for nm in ("hits", "last"):
+        for fld in ("k", "w"):
+            assert torch.equal(r.outputs[nm][fld], r0.outputs[nm][fld])
+    assert abs(float(d["tot"]) - (tp - tm_) / (2 * h)) <= 1e-3 * abs((tp - tm_) / (2 * h))
+
+
+def test_records_grad_matches_jvp(cuda):
+    """the adjoint with cotangents on both Records outputs and the Sum against the jvp's contraction (and a central
+    difference); a second call bitwise the same"""
+    f, w, keys = _setup()
+    a = np.float32(1.05)
+    rng = np.random.default_rng(5)
+    ct = {"tot": torch.tensor(0.3),
+          "hits": {"w": torch.from_numpy(rng.normal(size=CAP).astype(np.float32))},
+          "last": {"w": torch.from_numpy(rng.normal(size=len(w)).astype(np.float32))}}
+    g = f.grad(w, keys, a, wrt=2, cotangents=ct)
+    g2 = f.grad(w, keys, a, wrt=2, cotangents=ct)
+    _, d = f.jvp(w, keys, a, wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    want = (0.3 * float(d["tot"]) + float((ct["hits"]["w"].double() * d["hits"]["w"].cpu().double()).sum())
+            + float((ct["last"]["w"].double() * d["last"]["w"].cpu().double()).sum()))
+    assert abs(float(g) - want) <= 1e-5 * max(abs(want), 1.0)
+    assert torch.equal(g.view(torch.int32), g2.view(torch.int32))
+    r, gv = f.value_and_grad(w, keys, a, wrt=2, cotangents=ct)
+    torch.cuda.synchronize()
+    assert torch.equal(gv.view(torch.int32), g.view(torch.int32)) and int(r.stats["appended"]["last"]) == len(w)
+
+
+def test_records_grad_and_jvp_poison_on_overflow(cuda):
+    f, w, keys = _setup(cap=64)
+    g = f.grad(w, keys, np.float32(1.05), wrt=2, cotangents={"tot": torch.tensor(1.0)})
+    r, d = f.jvp(w, keys, np.float32(1.05), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    assert torch.isnan(g) and torch.isnan(d["hits"]["w"]).all() and torch.isnan(d["tot"])
+    assert int(r.stats["records_dropped"]["hits"]) > 0
+
+
+def test_records_replay_count_mismatch_flags(cuda):
+    """the negative control of the replay's append count (_records.py twin: a final k != cnt poisons): the adjoint
+    given one item's count off by one flags that item, and only it"""
+    f, w, keys = _setup(n=500)
+    a = np.float32(1.05)
+    L = f.lowered((w, keys, a))
+    fo = B.run(L.fwd, [w, keys], [a], consts=(64,))
+    ys = fo[len(L.fwd.tallies) + 1:]
+    prog = L.grad_program((0,))
+    pi = [w, keys]
+    for r, (nm, cap, _) in enumerate(L.fwd.records):
+        cnt = ys[L.n_results + r].clone()
+        if nm == "hits":
+            cnt[7] += 1
+        off = torch.cumsum(cnt.to(torch.int64), 0) - cnt.to(torch.int64)
+        pi += [cnt, off]
+    cts = [torch.zeros(())] + [torch.zeros(cap) for nm, cap, _ in L.fwd.records]
+    out = B.run(prog, pi, [a] + cts, consts=(64,))
+    torch.cuda.synchronize()
+    tr = out[-1].cpu().numpy()
+    assert tr[7] == 1 and tr.sum() == 1
