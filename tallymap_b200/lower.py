@@ -577,15 +577,17 @@ def forward_source(it, standalone=True, record=False):
         names = _names_pre(it)
         for (v, _), ld in zip(it.loads, src):
             lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
-        lines += _emit_code(tr.pre, names, emitter)
+        if recs:
+            # (records appended before the loop: the item's first ordinals)
+            lines.append("    c.item = item;")
+            lines += [f"    i32 a{r} = 0;" for r in range(len(recs))]
+        lines += _emit_code(tr.pre, names, emitter, appender=appender_for(lambda r: f"a{r}") if recs else None)
         for i in it.saved:
             lines.append(f"    c.p{i} = {names[i]};")
-        if recs:
-            lines.append("    c.item = item;")
         lines.append("    State s;")
         lines.append("    s.kc = 0;")
         for r in range(len(recs)):
-            lines.append(f"    s.a{r} = 0;")
+            lines.append(f"    s.a{r} = a{r};")
         if rec:
             lines.append("    s.me = ch.slot; s.gen = ch.gen; s.last = -1;" if "start_child" in head else
                          "    s.me = -1; s.gen = 0; s.last = -1;")
@@ -1343,7 +1345,7 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
         for v, ld in it.loads:
             lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
     lines += _emit_code(tr.pre, names, None, skip_emits=True)
-    rev = _Rev(act, tag="h")
+    rev = _Rev(act, tag="h", append_t=append_t if recs else None)
     for j, x in enumerate(tr.carry_in):
         if carry_act[j]:
             rev.add(x, f"a.cc{j}")
@@ -2096,7 +2098,11 @@ def jvp_source(it, wrt, L, contract=False):
                 lines.append(f"    float a{l} = 0.0f;")
         for (v, _), ld in zip(it.loads, src_):
             lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
-        lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter)
+        if recs:
+            lines.append("    c.item = item;")
+            lines += [f"    i32 rc{r} = 0;" for r in range(len(recs))]
+        lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter,
+                                appender=appender_for(lambda r: f"rc{r}") if recs else None)
         for i in it.saved:
             lines.append(f"    c.p{i} = {names[i]};")
         for i in act_saved:
@@ -2104,8 +2110,7 @@ def jvp_source(it, wrt, L, contract=False):
                 lines.append(f"    c.dp{i}_{l} = {tn[i][l] if i in tn else '0.0f'};")
         lines += ["    State s;", "    s.kc = 0;"]
         if recs:
-            lines.append("    c.item = item;")
-            lines += [f"    s.rc{r} = 0;" for r in range(len(recs))]
+            lines += [f"    s.rc{r} = rc{r};" for r in range(len(recs))]
         if contract:
             for l in range(L):
                 lines.append(f"    s.a{l} = a{l};")

@@ -696,9 +696,6 @@ def trace_item(fn, in_specs, n_per_item, specs, records=None, spawn=False):
     pre = tr.eqns[:st["pre_len"]]
     post = tr.eqns[st["pre_len"]:]
     keep = lambda xs: [x for x in xs if not isinstance(x, TallyToken)]
-    if any(e.prim == "append" for e in pre):
-        raise UnsupportedError("tallymap_b200.lang: append before the loop is not lowered "
-                               "(append in the loop or after it)")
     if any(e.prim == "spawn" for e in pre):
         raise UnsupportedError("tallymap_b200.lang: spawn before the loop is not lowered "
                                "(spawn in the loop or after it)")

@@ -367,3 +367,16 @@ def decay_records(t, w, key, a):
     k, w, t = tl.while_loop(lambda c: c[0] < 6, body, (0, w, t))
     t = t.append("last", {"k": k, "w": w})
     return t, k
+
+
+def pre_records(t, w, key, a):
+    """records before the loop, in it and after it into one output (the item's ordinals in that order)"""
+    t = t.append("log", {"k": -1, "w": w * a})
+    def body(c):
+        k, w, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.append("log", {"k": k, "w": w}, when=u < 0.5)
+        return k + 1, w * (0.6 + 0.3 * u) * a, t
+    k, w, t = tl.while_loop(lambda c: c[0] < 4, body, (0, w, t))
+    t = t.append("log", {"k": 99, "w": w * w})
+    return t, k

@@ -114,3 +114,37 @@ def test_records_replay_count_mismatch_flags(cuda):
     torch.cuda.synchronize()
     tr = out[-1].cpu().numpy()
     assert tr[7] == 1 and tr.sum() == 1
+
+
+def test_records_appended_before_the_loop(cuda):
+    """appends before the loop, in it and after it into one output: the canonical layout bitwise the IR evaluator's;
+    the tangents against a central difference; the adjoint against the jvp's contraction"""
+    from items_lang import pre_records
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    n, cap = 1000, 8192
+    rng = np.random.default_rng(3)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(9), n)
+    f = tm.vmap(pre_records, outputs={"log": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=cap)},
+                in_axes=(0, 0, None), max_steps=16)
+    tr = T.trace_item(pre_records, ["f32", "key", "f32"], 2, {}, {"log": (cap, (("k", "i32"), ("w", "f32")))})
+
+    def ev(a):
+        r = Evaluator(tr, 16).run([w, keys], [np.float32(a)])
+        return np.array([x[0] for x in r["records"]["log"]]), np.array([x[1] for x in r["records"]["log"]], np.float32)
+    a, h = 1.1, 1e-3
+    r, d = f.jvp(w, keys, np.float32(a), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    k0, w0 = ev(a)
+    m = len(k0)
+    assert int(r.stats["appended"]["log"]) == m and (k0 == -1).sum() == n and (k0 == 99).sum() == n
+    assert np.array_equal(r.outputs["log"]["k"].cpu().numpy()[:m], k0)
+    assert np.array_equal(r.outputs["log"]["w"].cpu().numpy()[:m].view(np.uint32), w0.view(np.uint32))
+    fd = (ev(a + h)[1].astype(np.float64) - ev(a - h)[1]) / (2 * h)
+    assert np.allclose(d["log"]["w"].cpu().numpy()[:m], fd, rtol=1e-3, atol=1e-4)
+    ct = torch.from_numpy(rng.normal(size=cap).astype(np.float32))
+    g = f.grad(w, keys, np.float32(a), wrt=2, cotangents={"log": {"w": ct}})
+    torch.cuda.synchronize()
+    want = float((ct.double() * d["log"]["w"].cpu().double()).sum())
+    assert abs(float(g) - want) <= 1e-5 * max(abs(want), 1.0)
