@@ -62,26 +62,41 @@ class Queue:
 
 @dataclasses.dataclass(frozen=True)
 class Records:
-    """a Records output (tallymap.Records, _api.py:98-170): Records({field: dtype}, capacity=C).  Items append with
-    t = t.append(name, {field: value}, when=...); Result.outputs[name] is {field: tensor[C]}: record k of item i at
-    slot offset[i] + k (offset the exclusive prefix sum of the per-item counts), slots past the last record zero;
-    stats['appended'][name] the true total.  More than C records poisons the call: float fields and every float
-    Sum NaN, integer fields -1, stats['records_dropped'][name] the excess."""
+    """a Records output (tallymap.Records, _api.py:98-170): Records({field: dtype}, capacity=C) or
+    Records({field: dtype}) (capacity None).  Items append with t = t.append(name, {field: value}, when=...);
+    Result.outputs[name] is {field: tensor}: record k of item i at slot offset[i] + k (offset the exclusive prefix sum
+    of the per-item counts); stats['appended'][name] the true total.
+      capacity C (one pass, _records.py): tensors of C slots, those past the last record zero.  More than C records
+        poisons the call: float fields and every float Sum NaN, integer fields -1, stats['records_dropped'][name]
+        the excess.
+      capacity None (count-then-fill, _api.py:138-148): the items run twice, a count pass (each item's record count)
+        and the fill pass (every output; record k of item i written straight to offset[i] + k): tensors of exactly
+        the total.  An item whose fill appends a different number of records than its count poisons the call like
+        an overflow, counted in stats['records_mismatch'][name]."""
     fields: tuple
-    capacity: int
+    capacity: Any
 
-    def __init__(self, fields, capacity):
+    def __init__(self, *args, fields=None, capacity=None):
+        for a in args:             # (the reference's Records(fields, capacity) in either order)
+            if isinstance(a, dict):
+                if fields is not None:
+                    raise TypeError("tallymap_b200.Records: fields given twice")
+                fields = a
+            elif a is None or isinstance(a, (int, np.integer)):
+                capacity = a
+            else:
+                raise TypeError(f"tallymap_b200.Records(fields, capacity): unexpected argument {a!r}")
         fl = []
-        for f, dt in sorted(fields.items()):
+        for f, dt in sorted((fields or {}).items()):
             if dt not in (torch.float32, torch.int32):
                 raise TypeError(f"tallymap_b200.Records: field {f!r}: float32 or int32")
             fl.append((f, dt))
         if not fl:
             raise TypeError("tallymap_b200.Records needs fields")
-        if not 1 <= int(capacity) <= 2 ** 31 - 1:
-            raise ValueError("tallymap_b200.Records: capacity in [1, 2^31 - 1]")
+        if capacity is not None and not 1 <= int(capacity) <= 2 ** 31 - 1:
+            raise ValueError("tallymap_b200.Records: capacity in [1, 2^31 - 1] or None")
         object.__setattr__(self, "fields", tuple(fl))
-        object.__setattr__(self, "capacity", int(capacity))
+        object.__setattr__(self, "capacity", None if capacity is None else int(capacity))
 
 
 class Result(NamedTuple):
@@ -139,6 +154,13 @@ def _poison(outs, bad):
     """NaN for every float output when `bad` (a select, so a clean call is bitwise unchanged: _api.py:916-925)."""
     return {n: (torch.where(bad, torch.full_like(v, float("nan")), v) if v.is_floating_point() else v)
             for n, v in outs.items()}
+
+
+def _poison_records(rec, bad):
+    """a Records output's fields when it overflowed or its fill disagreed with its count: float fields NaN, integer
+    fields -1 (as the one-pass canonical layout poisons)"""
+    return {n: torch.where(bad, torch.full_like(v, float("nan") if v.is_floating_point() else -1), v)
+            for n, v in rec.items()}
 
 
 class Mapped:
@@ -489,12 +511,71 @@ class MappedFn:
         L = self.lowered(args)
         pi, bc = self._split(args)
         p = L.fwd
+        if p.records and self._fill_needed():
+            # count-then-fill: the count pass, then the fill pass with every record at its canonical slot
+            cnts, offs, tots = self._counts(L, pi, bc, n_active)
+            fprog = self._sized(L.records_programs()[1], tots)
+            out = B.run(fprog, self._with_counts(pi, cnts, offs), bc, consts=(self.max_steps,), n_active=n_active)
+            return self._result(L, fprog, out, B.run.last["results"], fill=(cnts, tots))
         out = B.run(p, pi, bc, consts=(self.max_steps,), queue=self.spawn.capacity if self.spawn else None,
                     n_active=n_active)
         return self._result(L, p, out, B.run.last["results"])
 
-    def _result(self, L, p, out, raw):
-        """the Result of a forward launch's outputs (run()'s list; raw: its buffers by name)"""
+    def _fill_needed(self):
+        """whether a Records output has no capacity (count-then-fill)"""
+        return any(o[0] == "records" and o[1] is None for o in self.outputs.values())
+
+    def _counts(self, L, pi, bc, n_active=None):
+        """the count pass: per Records output (L.fwd.records' order) the items' record counts int32[N], their
+        canonical offsets int64[N] (the exclusive prefix sum) and the total (host ints: one synchronisation)"""
+        cprog = L.records_programs()[0]
+        out = B.run(cprog, pi, bc, consts=(self.max_steps,), n_active=n_active)
+        ys = out[len(cprog.tallies) + 1:]
+        cnts = [ys[L.n_results + r].clone() for r in range(len(L.fwd.records))]
+        offs = [torch.cumsum(c.to(torch.int64), 0) - c.to(torch.int64) for c in cnts]
+        tots = [int(t) for t in torch.stack([c.to(torch.int64).sum() for c in cnts]).cpu().tolist()]
+        return cnts, offs, tots
+
+    @staticmethod
+    def _sized(prog, tots):
+        """a fill program with each Records output's buffers sized to its total"""
+        return dataclasses.replace(prog, records=tuple((nm, max(t, 1), fl) for (nm, _, fl), t in zip(prog.records, tots)))
+
+    @staticmethod
+    def _with_counts(pi, cnts, offs):
+        return list(pi) + [x for c, o in zip(cnts, offs) for x in (c, o)]
+
+    def _fill_records(self, L, raw, ys, cnts, tots, lanes=0):
+        """a fill launch's Records outputs (raw: its buffers by name): ({name: {field: tensor}} -- the declared
+        capacity's slots, zeros past the last record, or the exact total without one --, {name: {float field:
+        tangent (lanes, size)}}, stats additions, a device bool: an output overflowed or an item's fill appended a
+        different number of records than its count)"""
+        recs, tans = {}, {}
+        st = {"appended": {}, "records_dropped": {}, "records_mismatch": {}}
+        bad = torch.zeros((), dtype=torch.bool, device=ys[0].device)
+        for r, (nm, _, fields) in enumerate(L.fwd.records):
+            cap, tot = self.outputs[nm][1], tots[r]
+            size = tot if cap is None else cap
+            keep = min(tot, size)
+
+            def take(buf, dt):
+                o = torch.zeros(size, dtype=dt, device=buf.device)
+                o[:keep] = buf[:keep]
+                return o
+            recs[nm] = {f: take(raw[f"{nm}.{f}"], dt) for f, dt in fields}
+            if lanes:
+                tans[nm] = {f: torch.stack([take(raw[f"{nm}.{f}#d{l}"], torch.float32) for l in range(lanes)])
+                            for f, dt in fields if dt == torch.float32}
+            mis = (ys[L.n_results + r] != cnts[r]).sum(dtype=torch.int32)
+            st["appended"][nm] = torch.tensor(tot, dtype=torch.int64, device=mis.device)
+            st["records_dropped"][nm] = torch.tensor(max(tot - size, 0), dtype=torch.int64, device=mis.device)
+            st["records_mismatch"][nm] = mis
+            bad = bad | (mis > 0) | (tot > size)
+        return recs, tans, st, bad
+
+    def _result(self, L, p, out, raw, fill=None):
+        """the Result of a forward launch's outputs (run()'s list; raw: its buffers by name); fill: (counts, totals)
+        of a count-then-fill launch"""
         nt = len(p.tallies)
         tallies = {t.name: v for t, v in zip(p.tallies, out[:nt])}
         stats_raw = out[nt]
@@ -505,17 +586,24 @@ class MappedFn:
         stats = {n: stats_raw[i] for i, n in enumerate(B.STATS)}
         stats["n_truncated"] = n_tr
         bad = _limits(p, stats)
-        if p.records:
+        recs = None
+        if p.records and fill is not None:
+            recs, _, st, over = self._fill_records(L, raw, ys, fill[0], fill[1])
+            stats.update(st)
+            bad = bad | over
+            recs = {nm: _poison_records(rec, over) for nm, rec in recs.items()}
+        elif p.records:
             counts = {nm: ys[L.n_results + r] for r, (nm, _, _) in enumerate(p.records)}
-            recs = B.canonical_records(p, raw, counts)
-            stats["appended"] = {nm: tot for nm, (_, tot) in recs.items()}
-            stats["records_dropped"] = {nm: torch.clamp(tot - cap, min=0)
-                                        for (nm, cap, _), (_, tot) in zip(p.records, recs.values())}
+            cr = B.canonical_records(p, raw, counts)
+            recs = {nm: rec for nm, (rec, _) in cr.items()}
+            tots = {nm: tot for nm, (_, tot) in cr.items()}
+            stats["appended"] = tots
+            stats["records_dropped"] = {nm: torch.clamp(tots[nm] - cap, min=0) for nm, cap, _ in p.records}
             over = any(int(v) > 0 for v in stats["records_dropped"].values())
             bad = bad | over
         outs = _poison(tallies, bad)
-        if p.records:
-            for nm, (rec, _) in recs.items():
+        if recs is not None:
+            for nm, rec in recs.items():
                 outs[nm] = rec if not bool(n_tr > 0) else _poison(rec, n_tr > 0)
         return Result(outs, self._per_item(L, per[:L.n_results]), trunc, stats)
 
@@ -550,20 +638,25 @@ class MappedFn:
         over = False
         if L.fwd.records:
             # (a Records output's cotangents sit at its canonical slots: the adjoint needs each item's record count
-            # and offset, so a forward launch runs first -- the reference's fill twin reads the primal's counts)
-            fout = B.run(L.fwd, pi, bc, consts=(self.max_steps,), n_active=n_active)
-            fys = fout[len(L.fwd.tallies) + 1:]
-            pi = list(pi)
-            for r, (nm, cap, fields) in enumerate(L.fwd.records):
-                cnt = fys[L.n_results + r]
-                pi += [cnt, torch.cumsum(cnt.to(torch.int64), 0) - cnt.to(torch.int64)]
-                over = over | (cnt.to(torch.int64).sum() > cap)
-            for nm, cap, fields in L.fwd.records:
+            # and offset, so the count pass runs first -- the reference's fill twin reads the primal's counts)
+            cnts, offs, tots = self._counts(L, pi, bc, n_active)
+            pi = self._with_counts(pi, cnts, offs)
+            sizes = {}
+            for r, (nm, _, fields) in enumerate(L.fwd.records):
+                cap = self.outputs[nm][1]
+                sizes[nm] = tots[r] if cap is None else cap
+                over = over or (cap is not None and tots[r] > cap)
+            for nm, _, fields in L.fwd.records:
                 given = cotangents.get(nm) or {}
                 for f, dt in fields:
                     if dt == torch.float32:
                         c = given.get(f)
-                        cts.append(torch.zeros(cap, dtype=torch.float32) if c is None else c)
+                        cts.append(torch.zeros(sizes[nm], dtype=torch.float32) if c is None else c)
+            # (an output without a capacity: its cotangents have the call's total records)
+            prog = dataclasses.replace(prog, bc=tuple(
+                dataclasses.replace(o, shape=(sizes[o.name[3:].split(".")[0]],))
+                if o.name.startswith("ct_") and "." in o.name and o.name[3:].split(".")[0] in sizes else o
+                for o in prog.bc))
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,), order=order,
                     rev_checkpoints=self.opts["rev_checkpoints"], n_active=n_active)
         ct = out[0].reshape(-1)
@@ -598,6 +691,13 @@ class MappedFn:
             raise ValueError(f"tallymap_b200: at most {lower.LANES_MAX} tangent lanes per launch")
         prog = L_.jvp_program(bpos, L)
         pi, bc = self._split(args)
+        fill = None
+        if prog.records and self._fill_needed():
+            # count-then-fill: the count pass, then the fill pass with the tangents beside the records
+            cnts, offs, tots = self._counts(L_, pi, bc, n_active)
+            fill = (cnts, tots)
+            prog = self._sized(L_.jvp_fill_program(bpos, L), tots)
+            pi = self._with_counts(pi, cnts, offs)
         out = B.run(prog, pi, list(bc) + [tan], consts=(self.max_steps,),
                     queue=self.spawn.capacity if self.spawn else None, n_active=n_active)
         raw = B.run.last["results"]
@@ -614,7 +714,12 @@ class MappedFn:
         stats["n_truncated"] = n_tr
         bad = _limits(prog, stats)
         rec_out, rec_t = {}, {}
-        if prog.records:
+        if fill is not None:
+            rec_out, rec_t, st, over = self._fill_records(L_, raw, ys, fill[0], fill[1], lanes=L)
+            stats.update(st)
+            bad = bad | over
+            rec_out = {nm: _poison_records(rec, over) for nm, rec in rec_out.items()}
+        elif prog.records:
             # the records and their fields' tangents in the canonical layout (moved together, _records.py canon);
             # a Records output past its capacity poisons every float output and tangent, as in the forward
             counts = {nm: ys[L_.n_results + r] for r, (nm, _, _) in enumerate(prog.records)}

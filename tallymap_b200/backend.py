@@ -82,6 +82,8 @@ class ItemProgram:
     vg_fallback: str = None         # a pipelined value-and-grad program: its kernel needs C >= max_steps (two heads
                                     # per thread); with a smaller C the launch uses this fused replay kernel instead
     records: tuple = ()             # Records outputs: ((name, capacity, ((field, torch dtype), ...)), ...)
+    records_fill: bool = False      # the fill pass of count-then-fill: records go straight to their canonical slots
+                                    # (offset + k from per-item operands), so the fields alone, sized by `capacity`
 
     @property
     def n_args(self):
@@ -104,9 +106,12 @@ class ItemProgram:
                 n64 = S * EXACT_WORDS + (S + 1) // 2
                 out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
         for name, cap, fields in self.records:
-            # the raw records (a slot per append, in claim order), their keys (item, ordinal) and the slot counter
+            # the raw records (a slot per append, in claim order), their keys (item, ordinal) and the slot counter;
+            # a fill pass: the fields alone, in the canonical layout
             for f, dt in fields:
                 out.append((f"{name}.{f}", cap * 4, dt, (cap,)))
+            if self.records_fill:
+                continue
             # (internal buffers are named with '#': a field may be called 'k')
             out.append((f"{name}#cid", cap * 4, torch.int32, (cap,)))
             out.append((f"{name}#k", cap * 4, torch.int32, (cap,)))

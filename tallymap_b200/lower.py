@@ -15,6 +15,7 @@ Launch layouts are the backend's (backend.ItemProgram): forward = [per-item][bro
 i32[3]][order] | [g f32[W]][exact words][ctl][stats] | [truncated][replay scratch].
 """
 import ctypes
+import dataclasses
 import hashlib
 import os
 
@@ -392,21 +393,32 @@ def _ref(x, names):
 
 
 # ------------------------------------------------------------------------------------------------ forward program
-def forward_source(it, standalone=True, record=False):
+def forward_source(it, standalone=True, record=False, mode="one"):
     """-> (C source of the forward ITEM + its extern "C" entry point, shared-memory bytes); standalone=False: the
     ITEM struct alone (for a combined program).  record (a spawning item): the recording forward of the tree adjoint
-    -- the forward's outputs plus a record of every child (_spawn_record_code) and each root's newest child"""
+    -- the forward's outputs plus a record of every child (_spawn_record_code) and each root's newest child.
+    mode, for Records outputs (tallymap.Records, _api.py:132-148): "one" -- one pass, a raw slot per append and the
+    record's key beside it (canonicalised after the launch); "count" -- the count pass of count-then-fill: the
+    per-item record counts alone (no records written, no emits); "fill" -- the fill pass: per output, the items'
+    counts and canonical offsets are per-item operands after the item's own, and record k of item i goes straight to
+    slot offset[i] + k while k < count[i] (an item appending a different number is seen by its count)"""
     tr = it.tr
     npi, nbc = len(it.pi), len(it.bc)
     sp = it.spawns
     rec = bool(record and sp)
+    count, fill = mode == "count", mode == "fill"
     lines = [('#include "tm_spawn.cuh"' if sp else "") + PRELUDE, "namespace tmb {", "struct GenFwd {"]
     # buffer indices: per-item, broadcast, consts, order | tallies, [exact words], [records], [ring sequence and
     # control words], ctl, stats | ys, [record counts], trunc, [ring]
+    recs = list(tr.records.items())         # [(name, (capacity, ((field, dtype), ...)))]
     idx = 0
     enum = []
     for j in range(npi):
         enum.append(f"kIn{j} = {idx}"); idx += 1
+    if fill:
+        for r in range(len(recs)):
+            enum.append(f"kRCnt{r} = {idx}"); idx += 1
+            enum.append(f"kROff{r} = {idx}"); idx += 1
     for k in range(nbc):
         enum.append(f"kBc{k} = {idx}"); idx += 1
     enum.append(f"kConsts = {idx}"); idx += 1
@@ -416,10 +428,13 @@ def forward_source(it, standalone=True, record=False):
     for t, (name, _) in enumerate(it.specs):
         if name in it.exact:
             enum.append(f"kX{t} = {idx}"); idx += 1
-    recs = list(tr.records.items())         # [(name, (capacity, ((field, dtype), ...)))]
     for r, (rname, (cap, fields)) in enumerate(recs):
+        if count:
+            continue
         for f in range(len(fields)):
             enum.append(f"kR{r}F{f} = {idx}"); idx += 1
+        if fill:
+            continue
         enum.append(f"kR{r}Cid = {idx}"); idx += 1
         enum.append(f"kR{r}K = {idx}"); idx += 1
         enum.append(f"kR{r}Ctr = {idx}"); idx += 1
@@ -487,9 +502,14 @@ def forward_source(it, standalone=True, record=False):
     for i in it.saved:
         ctx.append(f"    {CTYPE[it.vars[i].dtype]} p{i};")
     for r, (rname, (cap, fields)) in enumerate(recs):
-        for f, (fname, dt) in enumerate(fields):
-            ctx.append(f"    {CTYPE[dt]}* r{r}f{f};")
-        ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;", f"    i32* r{r}n;"]
+        if not count:
+            for f, (fname, dt) in enumerate(fields):
+                ctx.append(f"    {CTYPE[dt]}* r{r}f{f};")
+        if mode == "one":
+            ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;"]
+        if fill:
+            ctx += [f"    const i32* rcnt{r};", f"    const long long* roff{r};", f"    i32 rn{r};", f"    long long ro{r};"]
+        ctx.append(f"    i32* r{r}n;")
     if recs:
         ctx.append("    i64 item;")
     if rec:
@@ -527,11 +547,17 @@ def forward_source(it, standalone=True, record=False):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
     lines.append("    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);")
     for r, (rname, (cap, fields)) in enumerate(recs):
-        for f, (fname, dt) in enumerate(fields):
-            lines.append(f"    c.r{r}f{f} = static_cast<{CTYPE[dt]}*>(P.p[kR{r}F{f}]);")
-        lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);", f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
-                  f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);",
-                  f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);"]
+        if not count:
+            for f, (fname, dt) in enumerate(fields):
+                lines.append(f"    c.r{r}f{f} = static_cast<{CTYPE[dt]}*>(P.p[kR{r}F{f}]);")
+        if mode == "one":
+            lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);",
+                      f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
+                      f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);"]
+        if fill:
+            lines += [f"    c.rcnt{r} = static_cast<const i32*>(P.p[kRCnt{r}]);",
+                      f"    c.roff{r} = static_cast<const long long*>(P.p[kROff{r}]);"]
+        lines.append(f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);")
     if rec:
         lines += ["    c.rec = static_cast<i32*>(P.p[kRecord]);",
                   "    c.rgen = static_cast<unsigned short*>(P.p[kRecGen]);",
@@ -545,9 +571,19 @@ def forward_source(it, standalone=True, record=False):
     def appender_for(counter):
         def appender(rname, when_c, vals_c):
             """one record: the next raw slot of the output (one atomic, the counter keeps the true total), its
-            fields and its key (item, ordinal); -0.0 is stored as +0.0 (tallymap.Records)"""
+            fields and its key (item, ordinal); -0.0 is stored as +0.0 (tallymap.Records).  Count pass: the ordinal
+            alone; fill pass: the fields at the canonical slot offset + ordinal, while the ordinal is below the
+            item's count"""
             r = rindex[rname]
             cap, fields = tr.records[rname]
+            if count:
+                return f"if ({when_c}) {counter(r)} += 1;"
+            if fill:
+                st = [f"if ({when_c}) {{ if ({counter(r)} < c.rn{r}) {{ const long long s_ = c.ro{r} + {counter(r)};"]
+                for f, ((fname, dt), v) in enumerate(zip(fields, vals_c)):
+                    st.append(f" c.r{r}f{f}[s_] = {v}{' + 0.0f' if dt == T.F32 else ''};")
+                st.append(f" }} {counter(r)} += 1; }}")
+                return "".join(st)
             st = [f"if ({when_c}) {{ const unsigned long long o_ = atomicAdd(c.r{r}ctr, 1ull); "
                   f"if (o_ < {int(cap)}ull) {{"]
             for f, ((fname, dt), v) in enumerate(zip(fields, vals_c)):
@@ -581,7 +617,11 @@ def forward_source(it, standalone=True, record=False):
             # (records appended before the loop: the item's first ordinals)
             lines.append("    c.item = item;")
             lines += [f"    i32 a{r} = 0;" for r in range(len(recs))]
-        lines += _emit_code(tr.pre, names, emitter, appender=appender_for(lambda r: f"a{r}") if recs else None)
+            if fill:
+                lines += [f"    c.rn{r} = __ldg(&c.rcnt{r}[item]); c.ro{r} = __ldg(&c.roff{r}[item]);"
+                          for r in range(len(recs))]
+        lines += _emit_code(tr.pre, names, emitter, appender=appender_for(lambda r: f"a{r}") if recs else None,
+                            skip_emits=count)
         for i in it.saved:
             lines.append(f"    c.p{i} = {names[i]};")
         lines.append("    State s;")
@@ -639,7 +679,8 @@ def forward_source(it, standalone=True, record=False):
     if sp or split is None:
         names = _names_loop(it, tr.carry)
         lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"),
-                            spawner=_spawn_record_code(it, "s.gen", "s.last") if rec else _spawn_code)
+                            spawner=_spawn_record_code(it, "s.gen", "s.last") if rec else _spawn_code,
+                            skip_emits=count)
         lines += _assign_carry(it, names)
         lines.append("  }")
     if not sp:
@@ -655,7 +696,7 @@ def forward_source(it, standalone=True, record=False):
     if rec:
         lines.append("    i32 last_ = s.last;")
     lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"),
-                        spawner=_spawn_record_code(it, "s.gen", "last_") if rec else _spawn_code)
+                        spawner=_spawn_record_code(it, "s.gen", "last_") if rec else _spawn_code, skip_emits=count)
     if sp:
         # a child's per-item results are discarded (tallymap/_tally.py:285-286); its truncation is counted
         lines.append("    const bool tr_ = s.kc >= c.M && pred(c, s);")
@@ -1260,8 +1301,9 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
         out.append(f"{ind}if ({when}) {{")
         out.append(f"{ind}  a.ka{r} -= 1;")
         if took:
+            # (an output without a capacity -- count-then-fill -- holds every slot below the item's count)
             out.append(f"{ind}  const long long s_ = c.ro{r} + (long long)a.ka{r};")
-            out.append(f"{ind}  if (a.ka{r} >= 0 && s_ < {int(cap)}ll) {{")
+            out.append(f"{ind}  if (a.ka{r} >= 0{f' && s_ < {int(cap)}ll' if cap else ''}) {{")
             out += [f"{ind}    ra{k}_{f} = __ldg(&c.rct{r}f{f}[s_]);" for f, _ in took]
             out.append(f"{ind}  }}")
         out.append(f"{ind}}}")
@@ -1466,7 +1508,9 @@ class Lowered:
         self.name = name or getattr(fn, "__name__", "item")
         self.head, self.flags = options_source(math, min_blocks)
         self.math, self.min_blocks = math, min_blocks
-        recs = {k: (v[1], tuple(v[2])) for k, v in outputs.items() if v[0] == "records"}
+        # (a Records output without a capacity -- count-then-fill -- has capacity 0 in the one-pass program, which
+        # never runs for it)
+        recs = {k: (int(v[1] or 0), tuple(v[2])) for k, v in outputs.items() if v[0] == "records"}
         outputs = {k: v for k, v in outputs.items() if v[0] != "records"}
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
         exact = [k for k, v in outputs.items() if len(v) > 2 and v[2]]
@@ -1587,6 +1631,55 @@ class Lowered:
                                        queue_leaf_bytes=self._child_bytes(len(wrt)) if sp else 0)
             self.vgs[wrt] = prog
         return self.vgs[wrt]
+
+    def records_programs(self):
+        """count-then-fill (Records outputs without a capacity, _api.py:138-148): (the count pass -- the per-item
+        record counts, no records, no emits -- and the fill pass -- the forward's outputs, each record at its
+        canonical slot from the counts and offsets given as per-item operands after the item's own).  The fill
+        program's Records capacities are the placeholder 0: a call sets each to its total."""
+        from .backend import ItemProgram, Operand
+        if not self.fwd.records:
+            raise ValueError(f"tallymap_b200: item {self.name!r} has no Records outputs")
+        if getattr(self, "_rp", None) is None:
+            it = self.it
+            nrec = sum(len(fl) + 3 for _, _, fl in self.fwd.records)
+            src, smem = forward_source(it, mode="count")
+            kc = self._compile(src, self.name + "_count", self._fwd_nbuf - nrec, smem)
+            cnt = ItemProgram(self.name + "_count", kc, pi=self.pi, bc=self.bc, consts=("max_steps",),
+                              tallies=self.fwd.tallies, ys=self.fwd.ys, trunc=self.fwd.trunc)
+            src, smem = forward_source(it, mode="fill")
+            nr = len(self.fwd.records)
+            kf = self._compile(src, self.name + "_fill", self._fwd_nbuf - 3 * nr + 2 * nr, smem)
+            pi = self.pi + tuple(o for nm, _, _ in self.fwd.records
+                                 for o in (Operand(f"{nm}#count", (), torch.int32),
+                                           Operand(f"{nm}#offset", (), torch.int64)))
+            fil = ItemProgram(self.name + "_fill", kf, pi=pi, bc=self.bc, consts=("max_steps",),
+                              tallies=self.fwd.tallies, ys=self.fwd.ys, trunc=self.fwd.trunc,
+                              records=tuple((nm, 0, fl) for nm, _, fl in self.fwd.records), records_fill=True)
+            self._rp = (cnt, fil)
+        return self._rp
+
+    def jvp_fill_program(self, wrt, lanes):
+        """the fill pass of count-then-fill with L tangent lanes (jvp_source mode "fill"): operands as jvp_program's
+        with each Records output's counts and offsets after the per-item operands; tangent fields "field#d<lane>"
+        beside the fields, every capacity the placeholder 0"""
+        self._differentiable(wrt)
+        from .backend import ItemProgram, TSpec, Operand
+        key = ("fill", tuple(wrt), int(lanes))
+        if key not in self.jvps:
+            base = self.jvp_program(wrt, lanes)
+            src, smem = jvp_source(self.it, list(wrt), int(lanes), mode="fill")
+            records = tuple((nm, 0, fl) for nm, _, fl in base.records)
+            nr = len(records)
+            nx = sum(1 for t in base.tallies if t.exact)
+            nrec = sum(len(fl) for _, _, fl in records)
+            nbuf = len(self.pi) + 2 * nr + len(base.bc) + 2 + len(base.tallies) + nx + nrec + 2 + len(base.ys)
+            kid = self._compile(src, f"{self.name}_jvpfill{''.join(map(str, wrt))}x{lanes}", nbuf, smem)
+            pi = self.pi + tuple(o for nm, _, _ in records for o in (Operand(f"{nm}#count", (), torch.int32),
+                                                                      Operand(f"{nm}#offset", (), torch.int64)))
+            self.jvps[key] = dataclasses.replace(base, name=f"{self.name}_jvpfill", kernel=kid, pi=pi,
+                                                 records=records, records_fill=True)
+        return self.jvps[key]
 
     def rec_program(self):
         """the tree adjoint's recording forward (a spawning item; the reference's rec_primal): the forward's outputs,
@@ -1786,7 +1879,7 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
     return out
 
 
-def jvp_source(it, wrt, L, contract=False):
+def jvp_source(it, wrt, L, contract=False, mode="one"):
     """-> (C source of the forward ITEM with L tangent lanes of the broadcast operands bc[wrt], shared-memory bytes).
     Buffers: [per-item][broadcast][tangent seeds f32[L, W]][consts][order] | [tallies][tangent tallies f32[L, S] of
     the float tallies][ctl][stats] | [per-item results][truncated].
@@ -1794,7 +1887,9 @@ def jvp_source(it, wrt, L, contract=False):
     with the identity, each tangent emit contracted with the output's cotangent at its index into a per-item sum per
     lane, the sums emitted once per item into an exact W-bin tally.  Buffers: [per-item][broadcast][output
     cotangents of the float tallies][consts][order] | [tallies][ct f32[W]][ct's exact words][ctl][stats] |
-    [per-item results][truncated]"""
+    [per-item results][truncated].
+    mode="fill": Records outputs written by the fill pass of count-then-fill (forward_source's mode), the fields'
+    tangents beside them at the canonical slot"""
     tr = it.tr
     npi, nbc, W = len(it.pi), len(it.bc), len(wrt)
     if contract:
@@ -1805,6 +1900,7 @@ def jvp_source(it, wrt, L, contract=False):
     # Records outputs (forward mode proper only): each append writes its float fields' L tangents beside the fields,
     # at the same raw slot, so the canonical layout moves them with their records (tallymap/_records.py canon)
     recs = list(tr.records.items())         # [(name, (capacity, ((field, dtype), ...)))]
+    fill = mode == "fill"
     if recs and contract:
         raise LowerError("tallymap_b200.lower: Records outputs have no one-pass forward-mode value-and-grad")
     # a spawning item: a child carries its float per-item inputs' tangents (fl: their positions among the leaves)
@@ -1816,6 +1912,10 @@ def jvp_source(it, wrt, L, contract=False):
     enum = []
     for j in range(npi):
         enum.append(f"kIn{j} = {idx}"); idx += 1
+    if fill:
+        for r in range(len(recs)):
+            enum.append(f"kRCnt{r} = {idx}"); idx += 1
+            enum.append(f"kROff{r} = {idx}"); idx += 1
     for k in range(nbc):
         enum.append(f"kBc{k} = {idx}"); idx += 1
     if contract:
@@ -1849,6 +1949,8 @@ def jvp_source(it, wrt, L, contract=False):
             if dt == T.F32:
                 for l in range(L):
                     enum.append(f"kR{r}D{f}_{l} = {idx}"); idx += 1
+        if fill:
+            continue
         enum.append(f"kR{r}Cid = {idx}"); idx += 1
         enum.append(f"kR{r}K = {idx}"); idx += 1
         enum.append(f"kR{r}Ctr = {idx}"); idx += 1
@@ -1942,7 +2044,11 @@ def jvp_source(it, wrt, L, contract=False):
             ctx.append(f"    {CTYPE[dt]}* r{r}f{f};")
             if dt == T.F32:
                 ctx += [f"    float* r{r}d{f}_{l};" for l in range(L)]
-        ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;", f"    i32* r{r}n;"]
+        if fill:
+            ctx += [f"    const i32* rcnt{r};", f"    const long long* roff{r};", f"    i32 rn{r};", f"    long long ro{r};"]
+        else:
+            ctx += [f"    i32* r{r}cid;", f"    i32* r{r}k;", f"    unsigned long long* r{r}ctr;"]
+        ctx.append(f"    i32* r{r}n;")
     if recs:
         ctx.append("    i64 item;")
     ctx.append("  };")
@@ -2007,9 +2113,14 @@ def jvp_source(it, wrt, L, contract=False):
             lines.append(f"    c.r{r}f{f} = static_cast<{CTYPE[dt]}*>(P.p[kR{r}F{f}]);")
             if dt == T.F32:
                 lines += [f"    c.r{r}d{f}_{l} = static_cast<float*>(P.p[kR{r}D{f}_{l}]);" for l in range(L)]
-        lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);", f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
-                  f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);",
-                  f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);"]
+        if fill:
+            lines += [f"    c.rcnt{r} = static_cast<const i32*>(P.p[kRCnt{r}]);",
+                      f"    c.roff{r} = static_cast<const long long*>(P.p[kROff{r}]);"]
+        else:
+            lines += [f"    c.r{r}cid = static_cast<i32*>(P.p[kR{r}Cid]);",
+                      f"    c.r{r}k = static_cast<i32*>(P.p[kR{r}K]);",
+                      f"    c.r{r}ctr = static_cast<unsigned long long*>(P.p[kR{r}Ctr]);"]
+        lines.append(f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);")
     lines.append("  }")
     if contract:
         lines.append("  __device__ static void stage(const Params& P, unsigned char* smem) {")
@@ -2061,15 +2172,21 @@ def jvp_source(it, wrt, L, contract=False):
             stored as +0.0 (its tangent unchanged)"""
             r = rindex[rname]
             cap, fields = tr.records[rname]
-            st = [f"if ({when_c}) {{ const unsigned long long o_ = atomicAdd(c.r{r}ctr, 1ull); "
-                  f"if (o_ < {int(cap)}ull) {{"]
+            if fill:
+                st = [f"if ({when_c}) {{ if ({counter(r)} < c.rn{r}) {{ const long long o_ = c.ro{r} + {counter(r)};"]
+            else:
+                st = [f"if ({when_c}) {{ const unsigned long long o_ = atomicAdd(c.r{r}ctr, 1ull); "
+                      f"if (o_ < {int(cap)}ull) {{"]
             for f, ((fname, dt), v) in enumerate(zip(fields, vals_c)):
                 st.append(f" c.r{r}f{f}[o_] = {v}{' + 0.0f' if dt == T.F32 else ''};")
                 if dt == T.F32:
                     for l in range(L):
                         tv = vals_t[f][l] if vals_t[f] is not None else "0.0f"
                         st.append(f" c.r{r}d{f}_{l}[o_] = {tv};")
-            st.append(f" c.r{r}cid[o_] = (i32)c.item; c.r{r}k[o_] = {counter(r)}; }} {counter(r)} += 1; }}")
+            if fill:
+                st.append(f" }} {counter(r)} += 1; }}")
+            else:
+                st.append(f" c.r{r}cid[o_] = (i32)c.item; c.r{r}k[o_] = {counter(r)}; }} {counter(r)} += 1; }}")
             return "".join(st)
         return appender
 
@@ -2101,6 +2218,9 @@ def jvp_source(it, wrt, L, contract=False):
         if recs:
             lines.append("    c.item = item;")
             lines += [f"    i32 rc{r} = 0;" for r in range(len(recs))]
+            if fill:
+                lines += [f"    c.rn{r} = __ldg(&c.rcnt{r}[item]); c.ro{r} = __ldg(&c.roff{r}[item]);"
+                          for r in range(len(recs))]
         lines += _emit_code_jvp(tr.pre, names, tn, act, L, emitter, temitter,
                                 appender=appender_for(lambda r: f"rc{r}") if recs else None)
         for i in it.saved:

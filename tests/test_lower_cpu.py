@@ -950,3 +950,15 @@ def test_sort_argsort():
     want_s = np.take_along_axis(full, want_a, 1)
     assert np.array_equal(np.isnan(got_s), np.isnan(want_s))
     assert np.array_equal(got_s[~np.isnan(got_s)].view(np.uint32), want_s[~np.isnan(want_s)].view(np.uint32))
+
+
+def test_records_argument_forms():
+    """tallymap.Records(fields, capacity) in either order, capacity None (count-then-fill) by default; bad forms
+    raise"""
+    f32 = tm.api.torch.float32
+    assert tm.Records({"a": f32}, 5).capacity == 5 and tm.Records(5, {"a": f32}).capacity == 5
+    assert tm.Records({"a": f32}).capacity is None and tm.Records(fields={"a": f32}, capacity=None).capacity is None
+    for bad in (lambda: tm.Records({"a": f32}, 0), lambda: tm.Records({}, 4), lambda: tm.Records({"a": f32}, "x"),
+                lambda: tm.Records({"a": tm.api.torch.float64}, 4), lambda: tm.Records({"a": f32}, fields={"b": f32})):
+        with pytest.raises((TypeError, ValueError)):
+            bad()

@@ -148,3 +148,72 @@ def test_records_appended_before_the_loop(cuda):
     torch.cuda.synchronize()
     want = float((ct.double() * d["log"]["w"].cpu().double()).sum())
     assert abs(float(g) - want) <= 1e-5 * max(abs(want), 1.0)
+
+
+# ---------------------------------------------------------------------------------------------- count-then-fill
+def _pair(n=2000):
+    """the same item with a capacity-less Records output (count-then-fill) and with a large capacity (one pass)"""
+    from items_lang import decay_records
+    rng = np.random.default_rng(21)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(23), n)
+    mk = lambda cap: tm.vmap(decay_records, outputs={
+        "tot": tm.Sum(()), "hits": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=cap),
+        "last": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=n)}, in_axes=(0, 0, None), max_steps=64)
+    return mk(None), mk(CAP), w, keys
+
+
+def test_count_then_fill_forward(cuda):
+    """a Records output without a capacity: exactly the total records, each where the one-pass layout puts it; the
+    other outputs (a Sum, a Records output with a capacity) as the one-pass call's"""
+    ff, fo, w, keys = _pair()
+    a = np.float32(1.05)
+    r1, r2 = ff(w, keys, a), fo(w, keys, a)
+    torch.cuda.synchronize()
+    m = int(r2.stats["appended"]["hits"])
+    assert int(r1.stats["appended"]["hits"]) == m and r1.outputs["hits"]["w"].shape == (m,)
+    assert int(r1.stats["records_mismatch"]["hits"]) == 0 and int(r1.stats["records_dropped"]["hits"]) == 0
+    for fld in ("k", "w"):
+        assert torch.equal(r1.outputs["hits"][fld], r2.outputs["hits"][fld][:m])
+        assert torch.equal(r1.outputs["last"][fld], r2.outputs["last"][fld])
+    assert abs(float(r1.outputs["tot"]) - float(r2.outputs["tot"])) <= 1e-5 * abs(float(r2.outputs["tot"]))
+    assert torch.equal(r1.per_item, r2.per_item)
+
+
+def test_count_then_fill_jvp_and_grad(cuda):
+    """forward mode and the adjoint of a count-then-fill output against the one-pass ones: the tangents bitwise,
+    the gradient bitwise (the same cotangents at the same slots)"""
+    ff, fo, w, keys = _pair()
+    a = np.float32(1.05)
+    r1, d1 = ff.jvp(w, keys, a, wrt=2, tangents=[1.0])
+    r2, d2 = fo.jvp(w, keys, a, wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    m = int(r1.stats["appended"]["hits"])
+    assert d1["hits"]["w"].shape == (m,) and torch.equal(d1["hits"]["w"], d2["hits"]["w"][:m])
+    assert torch.equal(d1["last"]["w"], d2["last"]["w"])
+    rng = np.random.default_rng(8)
+    cth = rng.normal(size=CAP).astype(np.float32)
+    ctl = torch.from_numpy(rng.normal(size=len(w)).astype(np.float32))
+    g1 = ff.grad(w, keys, a, wrt=2, cotangents={"hits": {"w": torch.from_numpy(cth[:m])}, "last": {"w": ctl}})
+    g2 = fo.grad(w, keys, a, wrt=2, cotangents={"hits": {"w": torch.from_numpy(cth)}, "last": {"w": ctl}})
+    torch.cuda.synchronize()
+    assert torch.equal(g1.view(torch.int32), g2.view(torch.int32))
+
+
+def test_count_then_fill_with_an_overflowing_capacity_output(cuda):
+    """count-then-fill beside an output whose capacity is too small: that output's records are cut at its capacity
+    and poisoned (floats NaN, integers -1), every float output NaN, the capacity-less output's records intact"""
+    from items_lang import decay_records
+    rng = np.random.default_rng(21)
+    n = 500
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(23), n)
+    f = tm.vmap(decay_records, outputs={"tot": tm.Sum(()), "hits": tm.Records({"k": torch.int32, "w": torch.float32}),
+                                         "last": tm.Records({"k": torch.int32, "w": torch.float32}, capacity=n // 2)},
+                in_axes=(0, 0, None), max_steps=64)
+    r = f(w, keys, np.float32(1.05))
+    torch.cuda.synchronize()
+    assert int(r.stats["records_dropped"]["last"]) == n - n // 2 and r.outputs["last"]["w"].shape == (n // 2,)
+    assert torch.isnan(r.outputs["last"]["w"]).all() and (r.outputs["last"]["k"] == -1).all()
+    assert torch.isnan(r.outputs["tot"])
+    assert int(r.stats["records_mismatch"]["hits"]) == 0
