@@ -380,3 +380,54 @@ def pre_records(t, w, key, a):
     k, w, t = tl.while_loop(lambda c: c[0] < 4, body, (0, w, t))
     t = t.append("log", {"k": 99, "w": w * w})
     return t, k
+
+
+# Dormand-Prince 5(4): the tableau as Python floats (each rounded once to f32 where it meets an f32 value)
+_DP_A = ((1 / 5,), (3 / 40, 9 / 40), (44 / 45, -56 / 15, 32 / 9),
+         (19372 / 6561, -25360 / 2187, 64448 / 6561, -212 / 729),
+         (9017 / 3168, -355 / 33, 46732 / 5247, 49 / 176, -5103 / 18656))
+_DP_B = (35 / 384, 500 / 1113, 125 / 192, -2187 / 6784, 11 / 84)          # of k1, k3, k4, k5, k6
+_DP_E = (71 / 57600, -71 / 16695, 71 / 1920, -17253 / 339200, 22 / 525, -1 / 40)   # of k1, k3 .. k7
+
+
+def lorenz(t, sigma, rho, y0, item_id, beta):
+    """benchmark configuration 4's item as a tallymap user writes it (the hand-lowered csrc/items_ode.cuh states the
+    same source): Lorenz systems integrated by adaptive Dormand-Prince 5(4) on t in [0, 10], every linear
+    combination summed left to right"""
+    def f(y):
+        return (sigma * (y[1] - y[0]), y[0] * (rho - y[2]) - y[1], y[0] * y[1] - beta * y[2])
+
+    def lin(cs, ks, j):
+        acc = cs[0] * ks[0][j]
+        for c, k in zip(cs[1:], ks[1:]):
+            acc = acc + c * k[j]
+        return acc
+
+    def axpy(y, hh, d):
+        return tuple(y[j] + hh * d[j] for j in range(3))
+
+    def body(c):
+        k, tt, h, ya, yb, yc, ka, kb, kc, t = c
+        y, k1 = (ya, yb, yc), (ka, kb, kc)
+        hh = tl.minimum(h, 10.0 - tt)
+        ks = [k1]
+        for row in _DP_A:
+            ks.append(f(axpy(y, hh, tuple(lin(row, ks, j) for j in range(3)))))
+        k1_, k2, k3, k4, k5, k6 = ks
+        y5 = axpy(y, hh, tuple(lin(_DP_B, (k1_, k3, k4, k5, k6), j) for j in range(3)))
+        k7 = f(y5)
+        e = tuple(hh * lin(_DP_E, (k1_, k3, k4, k5, k6, k7), j) for j in range(3))
+        q = tuple(e[j] / (1e-9 + 1e-6 * tl.maximum(tl.abs(y[j]), tl.abs(y5[j]))) for j in range(3))
+        err = tl.sqrt((q[0] * q[0] + q[1] * q[1] + q[2] * q[2]) / 3.0)
+        ok = err <= 1.0
+        fac = tl.stop_gradient(tl.clip(0.9 * err ** -0.2, 0.2, 10.0))
+        yn = tuple(tl.where(ok, y5[j], y[j]) for j in range(3))
+        kn = tuple(tl.where(ok, k7[j], k1[j]) for j in range(3))
+        return (k + 1, tl.where(ok, tt + hh, tt), hh * fac) + yn + kn + (t,)
+    y = (y0[0], y0[1], y0[2])
+    c = tl.while_loop(lambda c: c[1] < 10.0, body, (0, 0.0, 1e-3) + y + f(y) + (t,))
+    k, yf, t = c[0], c[3:6], c[9]
+    for j in range(3):
+        t = t.add("final", (item_id, j), yf[j])
+    t = t.add("mean_z", 0, yf[2] / 1048576.0)
+    return t, k
