@@ -600,7 +600,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
             if pv:
                 return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
             return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
-                    f"else fatom(&c.g{t}[b_], {v_c}); }}")
+                    f"else fatom_warp_window(c.g{t}, nullptr, b_, -1, {v_c}); }}")
         tgt = f"c.s{t}" if pv else f"c.g{t}"
         return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
                 f"else if ({v_c}) atomicAdd(&{tgt}[b_], {v_c}); }}")
@@ -757,6 +757,9 @@ def _pred_fn(it):
 
 
 DRAW_UNROLL = 4      # steps drawn ahead per iteration (tm_runtime.cuh run_step) when the body's draws allow it
+DRAW_LIVE_MAX = 8    # at most this many drawn values held across the unrolled steps (DRAW_UNROLL x the values a step
+                     # keeps): the walk keeps two a step (8 held; the draw-ahead pays there), the photon four uniforms
+                     # and more (16+ held beside a heavy step: its forward 48 -> 99 ms), so it draws step by step
 _DRAW_PRIMS = ("threefry", "bits", "uniform01")
 
 
@@ -765,7 +768,8 @@ def _draw_split(it):
     operands, literals and the step counters (carries equal to the step index): their values at step kc + j are
     known before step kc runs, so the runtime can evaluate several steps' worth together (independent threefry
     chains; tm_runtime.cuh, run_step).  -> (draw equations, the other equations, ids of draw values the others or
-    the carry update read) or None when the draws hold no threefry (nothing worth drawing ahead)."""
+    the carry update read) or None when the draws hold no threefry (nothing worth drawing ahead) or more values
+    than DRAW_LIVE_MAX would hold across the unrolled steps."""
     tr = it.tr
     if it.spawns or tr.records:
         return None
@@ -782,6 +786,8 @@ def _draw_split(it):
     if not any(e.prim in _DRAW_PRIMS for e in draws):
         return None
     live = sorted(dset & (_uses(rest) | _ids(tr.body_out)))
+    if DRAW_UNROLL * len(live) > DRAW_LIVE_MAX:
+        return None
     return draws, rest, live
 
 
@@ -2144,7 +2150,7 @@ def jvp_source(it, wrt, L, contract=False, mode="one"):
             if pv:
                 return f"SumPriv<{S}>::emit(c.s{t}, c.stats, {idx_c}, {v_c});"
             return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
-                    f"else fatom(&c.g{t}[b_], {v_c}); }}")
+                    f"else fatom_warp_window(c.g{t}, nullptr, b_, -1, {v_c}); }}")
         tgt = f"c.s{t}" if pv else f"c.g{t}"
         return (f"{{ const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); "
                 f"else if ({v_c}) atomicAdd(&{tgt}[b_], {v_c}); }}")

@@ -431,3 +431,36 @@ def lorenz(t, sigma, rho, y0, item_id, beta):
         t = t.add("final", (item_id, j), yf[j])
     t = t.add("mean_z", 0, yf[2] / 1048576.0)
     return t, k
+
+
+def photon(t, key, mu_a, mu_s):
+    """benchmark configuration 3's item as a tallymap user writes it (csrc/items_photon.cuh states the same source):
+    a photon random-walking through a 64^3 slab, Henyey-Greenstein scattering (g = 0.9), roulette below 1e-3"""
+    g = 0.9
+    mu_t = mu_a + mu_s
+    albedo, frac = mu_s / mu_t, mu_a / mu_t
+
+    def body(c):
+        k, px, py, pz, dx, dy, dz, w, alive, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k), (4,))
+        s = (-tl.log(1.0 - u[0])) / mu_t
+        px, py, pz = px + s * dx, py + s * dy, pz + s * dz
+        inside = (px >= 0.0) & (px < 64.0) & (py >= 0.0) & (py < 64.0) & (pz >= 0.0) & (pz < 64.0)
+        ix, iy, iz = (tl.clip(q.astype(tl.int32), 0, 63) for q in (px, py, pz))
+        t = t.add("dep", (ix, iy, iz), tl.where(inside, w * frac, 0.0))
+        w1 = w * albedo
+        tmp = (1 - g * g) / ((1 - g) + (2 * g) * u[1])
+        cos_t = tl.clip(((1 + g * g) - tmp * tmp) / (2 * g), -1.0, 1.0)
+        sin_t = tl.sqrt(1.0 - cos_t * cos_t)
+        phi = (2 * 3.141592653589793) * u[2]
+        sp, cp = tl.sin(phi), tl.cos(phi)
+        r = tl.sqrt(1.0 - dz * dz)
+        polar = tl.abs(dz) > 0.99999
+        ndx = tl.where(polar, sin_t * cp, (sin_t * ((dx * dz) * cp - dy * sp)) / r + dx * cos_t)
+        ndy = tl.where(polar, sin_t * sp, (sin_t * ((dy * dz) * cp + dx * sp)) / r + dy * cos_t)
+        ndz = tl.where(polar, cos_t * tl.where(dz > 0.0, 1.0, -1.0), ((-sin_t) * cp) * r + dz * cos_t)
+        low, survive = w1 < 1e-3, u[3] < 0.1
+        w = tl.where(low, tl.where(survive, w1 * 10.0, 0.0), w1)
+        return k + 1, px, py, pz, ndx, ndy, ndz, w, inside & ~(low & ~survive), t
+    c = tl.while_loop(lambda c: c[8], body, (0, 32.0, 32.0, 0.0, 0.0, 0.0, 1.0, 1.0, True, t))
+    return c[9], c[0]
