@@ -222,7 +222,8 @@ class Evaluator:
         for e in eqns:
             a = [self._val(x, env) for x in e.ins]
             if e.prim == "emit":
-                out["emits"].append((e.params["tally"], a[0], a[1]))
+                if len(a) < 3 or a[2]:              # (a third operand: the predicate of a write in a cond branch)
+                    out["emits"].append((e.params["tally"], a[0], a[1]))
                 continue
             if e.prim == "append":
                 if a[0]:

@@ -7,7 +7,8 @@ over a per-item vector, random.bernoulli); the inverse trigonometric, hyperbolic
 erfinv primitives (random.normal over erfinv as jax.random forms it, random.exponential, gumbel, categorical,
 randint), ceil, log10, logistic, isfinite and the other jax.numpy compositions below; small vectors with jax.numpy's
 elementwise semantics (trace.Vec: array, stack, dot, reductions, a traced index read as jnp does); broadcast tables
-read by traced indices (trace.Table); cond / switch of effect-free branches and fori_loop / scan of static lengths.
+read by traced indices (trace.Table); cond / switch (both branches traced, results selected, a branch's t.add /
+t.append / t.spawn made only where it is taken) and fori_loop / scan of static lengths.
 
     from tallymap_b200 import lang as tl
 
@@ -24,6 +25,8 @@ read by traced indices (trace.Table); cond / switch of effect-free branches and 
 Transcendentals are the backend's shared f32 math (identical on the host oracle and the device); f32 -> int32
 conversion truncates toward zero, saturating, NaN -> 0 (the reference's _rz conversions).
 """
+import builtins
+
 from . import trace as T
 
 float32, int32, uint32, bool_ = "float32", "int32", "uint32", "bool"
@@ -240,8 +243,10 @@ def where(c, a, b):
     return T._cur().emit("select", [c, a, b], [a.dtype])[0]
 
 
-def _branch_select(pick, results):
-    """the elementwise selection of branch results of one structure: pick(j) -> bool Var, branch j taken"""
+def _branch_select(picks, results):
+    """the elementwise selection of branch results of one structure: picks[j] -> bool, branch j taken.  A leaf that
+    is not a value (the tally handle, a tally of the jaxpr front end) passes through when every branch returns that
+    same object, as a branch that writes the tally and returns it, or returns it untouched, does"""
     flat = [T._flatten(r) for r in results]
     leaves0, rebuild = flat[0]
     for lv, _ in flat[1:]:
@@ -249,44 +254,108 @@ def _branch_select(pick, results):
             raise T.TraceError("tallymap_b200.lang.cond: the branches return different structures")
     out = []
     for k in range(len(leaves0)):
-        r = flat[0][0][k]
-        for j in range(1, len(flat)):
-            r = where(pick(j), flat[j][0][k], r)
+        xs = [f[0][k] for f in flat]
+        if builtins.any(isinstance(x, T.TallyToken) for x in xs):
+            if builtins.any(x is not xs[0] for x in xs[1:]):
+                raise T.TallyError("tallymap_b200.lang.cond: the branches must use each tally the same way (write "
+                                   "it and return it, or return it untouched) (tallymap/_rewrite.py:178-182)")
+            out.append(xs[0])
+            continue
+        r = xs[0]
+        for j in range(1, len(xs)):
+            r = where(picks[j]() if isinstance(picks[j], _Pick) else picks[j], xs[j], r)
         out.append(r)
     return rebuild(out)
 
 
-def _branches(funs, operands):
-    """trace each branch on the same operands; a branch may not touch the tally (lax.cond of effect-free
-    branches: under vmap both run and a select keeps one, as jax does)"""
+_EFFECTS = ("emit", "append", "spawn")
+
+
+class _Pick:
+    """a branch predicate formed on first use: no equation for a branch whose result and effects need none"""
+
+    def __init__(self, make):
+        self.make, self.v = make, None
+
+    def __call__(self):
+        if self.v is None:
+            self.v = self.make()
+        return self.v
+
+
+def _predicate(tr, n0, taken):
+    """make the effects traced into tr.eqns[n0:] (one branch) happen only where `taken` (a bool): an emit carries
+    the predicate as a third operand, an append's and a spawn's `when` is ANDed with it (a nested branch's own
+    predicate included).  The branches of a lax.cond run as straight-line code, their results selected (as jax does
+    under vmap); the reference's backends run only the taken branch's t.add / t.spawn / t.append
+    (tallymap/_rewrite.py:573-598 threads the tally through lax.switch), and the predicate gives the same"""
+    if isinstance(taken, _Pick):
+        # (formed from values defined before the branch: its equations go in at the branch's start)
+        m = len(tr.eqns)
+        taken = taken()
+        new = tr.eqns[m:]
+        del tr.eqns[m:]
+        tr.eqns[n0:n0] = new
+    out = tr.eqns[:n0]
+    for e in tr.eqns[n0:]:
+        if e.prim not in _EFFECTS:
+            out.append(e)
+            continue
+        k = 2 if e.prim == "emit" else 0
+        old = e.ins[k] if len(e.ins) > k else T.Lit(True, T.BOOL)
+        if isinstance(taken, T.Lit) and not taken.value or isinstance(old, T.Lit) and not old.value:
+            continue                                   # (never taken: the effect is gone)
+        if isinstance(taken, T.Lit):
+            w = old
+        elif isinstance(old, T.Lit):
+            w = taken
+        else:
+            w = tr.new(T.BOOL)
+            out.append(T.Eqn("and", [old, taken], [w], {}))
+        ins = list(e.ins)
+        if k < len(ins):
+            ins[k] = w
+        elif not isinstance(w, T.Lit):
+            ins.append(w)
+        out.append(T.Eqn(e.prim, ins, e.outs, e.params))
+    tr.eqns[:] = out
+
+
+def _branches(funs, operands, picks):
+    """trace each branch on the same operands, its effects (t.add, t.append, t.spawn) predicated on picks[j]"""
     tr = T._cur()
-    n0 = len(tr.eqns)
-    res = [f(*operands) for f in funs]
-    if any(e.prim in ("emit", "append", "spawn") for e in tr.eqns[n0:]) or \
-            any(isinstance(x, T.TallyToken) for r in res for x in T._flatten(r)[0]):
-        raise T.UnsupportedError("tallymap_b200.lang.cond: a branch that writes the tally is not lowered (select "
-                                 "the value and index, and write once outside the branches)")
+    res = []
+    for f, taken in zip(funs, picks):
+        n0 = len(tr.eqns)
+        res.append(f(*operands))
+        if builtins.any(e.prim in _EFFECTS for e in tr.eqns[n0:]):
+            _predicate(tr, n0, taken)
     return res
 
 
 def cond(pred, true_fun, false_fun, *operands):
-    """lax.cond of effect-free branches: both traced, the results selected elementwise by pred"""
+    """lax.cond: both branches traced, their results selected elementwise by pred, their tally writes made only by
+    the taken one"""
     pred = T._lit(pred)
     if pred.dtype != T.BOOL:
         raise T.TraceError("tallymap_b200.lang.cond: the predicate must be bool")
-    f, t = _branches((false_fun, true_fun), operands)
-    return _branch_select(lambda j: pred, (f, t))
+    npred = _Pick(lambda: ~pred) if isinstance(pred, T.Var) else T.Lit(not pred.value, T.BOOL)
+    f, t = _branches((false_fun, true_fun), operands, (npred, pred))
+    return _branch_select((npred, pred), (f, t))
 
 
 def switch(index, branches, *operands):
-    """lax.switch of effect-free branches: the index clamped into range, each branch traced, a chain of selects"""
+    """lax.switch: the index clamped into range, each branch traced, a chain of selects; the tally writes made only
+    by the taken branch"""
     index = T._lit(index)
     if index.dtype != T.I32:
         raise T.TraceError("tallymap_b200.lang.switch: the index must be int32")
     n = len(branches)
     idx = clip(index, 0, n - 1) if isinstance(index, T.Var) else T.Lit(max(0, min(n - 1, int(index.value))), T.I32)
-    res = _branches(branches, operands)
-    return _branch_select(lambda j: idx == j if isinstance(idx, T.Var) else T.Lit(idx.value == j, T.BOOL), res)
+    picks = [_Pick(lambda j=j: idx == j) if isinstance(idx, T.Var) else T.Lit(idx.value == j, T.BOOL)
+             for j in range(n)]
+    res = _branches(branches, operands, picks)
+    return _branch_select(picks, res)
 
 
 def fori_loop(lower, upper, body_fun, init_val):

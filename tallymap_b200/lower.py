@@ -374,7 +374,9 @@ def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=N
             continue
         if e.prim == "emit":
             if not skip_emits:
-                out.append(indent + emitter(e.params["tally"], a[0], a[1]))
+                st = emitter(e.params["tally"], a[0], a[1])
+                # (a third operand: the emit's predicate, a write inside a lax.cond branch)
+                out.append(indent + (f"if ({a[2]}) {{ {st} }}" if len(a) > 2 else st))
             continue
         if e.prim == "threefry":
             o0, o1 = e.outs
@@ -969,11 +971,12 @@ class _Rev:
                     self.append_t(self, e, names)
                 continue
             if e.prim == "emit":
-                idx, v = e.ins
+                idx, v = e.ins[:2]
                 if isinstance(v, T.Var) and v.id in self.active and e.params["tally"] in ct_tally:
                     ptr, S = ct_tally[e.params["tally"]][:2]
                     i = _ref(idx, names)
-                    self.add(v, f"(((u32)({i}) < {S}u) ? {ptr}[{i}] : 0.0f)")
+                    w = f"({_ref(e.ins[2], names)}) && " if len(e.ins) > 2 else ""
+                    self.add(v, f"(({w}(u32)({i}) < {S}u) ? {ptr}[{i}] : 0.0f)")
                 continue
             if not e.outs or e.outs[0].id not in self.ct:
                 continue
@@ -1868,7 +1871,8 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
             v = e.ins[1]
             if isinstance(v, T.Var) and v.id in tnames:
                 for l in range(L):
-                    out.append(indent + temitter(e.params["tally"], l, a[0], tnames[v.id][l]))
+                    st = temitter(e.params["tally"], l, a[0], tnames[v.id][l])
+                    out.append(indent + (f"if ({a[2]}) {{ {st} }}" if len(a) > 2 else st))
             continue
         if not e.outs or e.outs[0].id not in act or e.outs[0].dtype != T.F32:
             continue

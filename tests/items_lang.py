@@ -464,3 +464,53 @@ def photon(t, key, mu_a, mu_s):
         return k + 1, px, py, pz, ndx, ndy, ndz, w, inside & ~(low & ~survive), t
     c = tl.while_loop(lambda c: c[8], body, (0, 32.0, 32.0, 0.0, 0.0, 0.0, 1.0, 1.0, True, t))
     return c[9], c[0]
+
+
+def branch_writes(t, x, key, a):
+    """tally writes inside lax.cond / lax.switch branches, made by the taken branch only (the reference threads the
+    tally through lax.switch, tallymap/_rewrite.py:573-598): per step a switch on a draw adds to bin 0, to bin 1 or,
+    in its last branch, appends a record through a nested cond when x < 0.25; a cond adds a * x to bin 3 above a
+    half and 1 to bin 2 below; after the loop, bin 4 takes x when the walk ran its 40 steps"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        j = (u * 3.0).astype(tl.int32)
+        t = tl.switch(j, [lambda tt: tt.add("h", 0, x * a),
+                          lambda tt: tt.add("h", 1, a * a),
+                          lambda tt: tl.cond(x < 0.25, lambda t2: t2.append("low", {"k": k, "x": x}),
+                                             lambda t2: t2, tt)], t)
+        t = tl.cond(x > 0.5, lambda tt: tt.add("h", 3, a * x), lambda tt: tt.add("h", 2, 1.0), t)
+        return k + 1, x + 0.05 * (2.0 * u - 1.0), t
+    k, x, t = tl.while_loop(lambda c: (c[0] < 40) & (c[1] >= 0.0) & (c[1] <= 1.0), body, (0, x, t))
+    t = tl.cond(k == 40, lambda tt: tt.add("h", 4, x), lambda tt: tt, t)
+    return t, k
+
+
+def branch_writes_where(t, x, key, a):
+    """branch_writes written without branches: each write at its bin every step, its value selected to zero (and a
+    record's `when`) where the branch is not taken -- the same sums, records and gradients"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        j = tl.clip((u * 3.0).astype(tl.int32), 0, 2)
+        t = t.add("h", 0, tl.where(j == 0, x * a, 0.0))
+        t = t.add("h", 1, tl.where(j == 1, a * a, 0.0))
+        t = t.append("low", {"k": k, "x": x}, when=(j == 2) & (x < 0.25))
+        t = t.add("h", 3, tl.where(x > 0.5, a * x, 0.0))
+        t = t.add("h", 2, tl.where(x > 0.5, 0.0, 1.0))
+        return k + 1, x + 0.05 * (2.0 * u - 1.0), t
+    k, x, t = tl.while_loop(lambda c: (c[0] < 40) & (c[1] >= 0.0) & (c[1] <= 1.0), body, (0, x, t))
+    t = t.add("h", 4, tl.where(k == 40, x, 0.0))
+    return t, k
+
+
+def spawn_decay_cond(t, g, w, key, a):
+    """spawn_decay with its child spawned from inside a lax.cond branch instead of by `when`"""
+    def body(c):
+        k, w, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        t = t.add("Q", k % 8, a * w * u)
+        return k + 1, w * 0.9, t
+    k, w, t = tl.while_loop(lambda c: c[0] < 3, body, (0, w, t))
+    t = tl.cond(g < 2, lambda tt: tt.spawn((g + 1, w * a, tl.random.fold_in(key, 7))), lambda tt: tt, t)
+    return t, k

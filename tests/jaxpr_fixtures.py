@@ -86,8 +86,23 @@ def uniform_pjit():
     return ClosedJaxpr(Jaxpr([q, r, s], [bd], eqns))
 
 
-def quickstart(cap=None):
-    """the quickstart item's closed jaxpr; cap: retrace(cap=max_steps)'s form (loop counter + truncated result)"""
+def _gated_emit(bx, gate, bh, bf, bh2, bi):
+    """`t = lax.cond(x > gate, lambda t: t.add("hist", bin, v), lambda t: t, t)` as jax writes it: the predicate
+    converted to an int32 branch index, the branches (false first) taking the closed-over bin and value and the
+    tally, the false branch returning its tally operand"""
+    cp, ci = Var(B), Var(I)
+    fi, fv, fh = Var(I), Var(F), Var(F, (16,))
+    ti, tv, th, to = Var(I), Var(F), Var(F, (16,)), Var(F, (16,))
+    false_b = ClosedJaxpr(Jaxpr([fi, fv, fh], [fh], []))
+    true_b = ClosedJaxpr(Jaxpr([ti, tv, th], [to], [Eqn("tallymap_emit", [th, ti, tv], [to])]))
+    return [Eqn("gt", [bx, Literal(gate, F)], [cp]),
+            Eqn("convert_element_type", [cp], [ci], new_dtype="int32", weak_type=False),
+            Eqn("cond", [ci, bf, bh2, bh], [bi], branches=(false_b, true_b))]
+
+
+def quickstart(cap=None, gate=None):
+    """the quickstart item's closed jaxpr; cap: retrace(cap=max_steps)'s form (loop counter + truncated result);
+    gate: the emit inside a lax.cond branch, made only on steps that start above x = gate"""
     hist, x0, key, theta = Var(F, (16,)), Var(F), Var(U, (2,)), Var(F)
     # body: consts (key, theta), carry ([cnt,] k, x, hist)
     bkey, btheta = Var(U, (2,)), Var(F)
@@ -104,7 +119,8 @@ def quickstart(cap=None):
                  Eqn("convert_element_type", [be], [bf], new_dtype="int32", weak_type=False),
                  Eqn("sub", [Literal(1.0, F), bx], [bg]),
                  Eqn("mul", [btheta, bg], [bh2]),
-                 Eqn("tallymap_emit", [bh, bf, bh2], [bi]),
+                 *([Eqn("tallymap_emit", [bh, bf, bh2], [bi])] if gate is None else
+                   _gated_emit(bx, gate, bh, bf, bh2, bi)),
                  Eqn("add", [bk, Literal(1, I)], [bj]),
                  Eqn("mul", [Literal(0.5, F), p], [bk2]),
                  Eqn("add", [Literal(0.5, F), bk2], [bl]),

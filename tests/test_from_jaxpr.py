@@ -39,6 +39,33 @@ def test_quickstart_jaxpr_against_oracle(orc):
     assert np.array_equal(rq["sums"]["hist"].view(np.uint32), r["sums"]["hist"].view(np.uint32))
 
 
+def test_emit_inside_a_cond_branch():
+    """the reference's `t = lax.cond(pred, lambda t: t.add(...), lambda t: t, t)` (the tally threaded through a
+    cond, tallymap/_rewrite.py:173-185, 573-598): the emit is made only where its branch is taken -- the IR equal
+    to the same item written with tallymap_b200.lang and a select of the value, its histogram bitwise"""
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import lang as tl
+    fn, specs = FJ.item_function(J.quickstart(gate=0.3), ["hist"], 2)
+    tr = T.trace_item(fn, specs, 2, SPECS)
+    (em,) = [e for e in tr.body if e.prim == "emit"]
+    assert len(em.ins) == 3 and em.ins[2].dtype == T.BOOL
+
+    def gated(t, x, key, theta):
+        def body(c):
+            k, x, t = c
+            u = tl.random.uniform(tl.random.fold_in(key, k))
+            t = t.add("hist", (x * 16).astype(tl.int32), tl.where(x > 0.3, theta * (1 - x), 0.0))
+            return k + 1, x * (0.5 + 0.5 * u), t
+        k, x, t = tl.while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
+        return t, k
+    x, k = _inputs(3000)
+    r = Evaluator(tr, 100).run([x, k], [2.0])
+    rq = Evaluator(T.trace_item(gated, ["f32", "key", "f32"], 2, SPECS), 100).run([x, k], [2.0])
+    assert np.array_equal(rq["results"][0], r["results"][0])
+    assert np.array_equal(rq["sums"]["hist"].view(np.uint32), r["sums"]["hist"].view(np.uint32))
+    assert r["sums"]["hist"][:4].max() == 0.0 and r["sums"]["hist"][5:].min() > 0.0
+
+
 def test_retraced_program_carries_its_own_cap(orc):
     """the reference backend receives retrace(cap)'s program: its loop counter stops the loop and its own
     `truncated` is the second per-item result, equal to the oracle's flags at max_steps = 3"""

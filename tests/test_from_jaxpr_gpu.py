@@ -41,3 +41,26 @@ def test_jaxpr_item_gradient_bitwise(cuda, orc):
     g = f.grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.from_numpy(ct)})
     ref = orc.q1_grad(x, k, 2.0, ct)
     assert np.array_equal(np.float32(g.cpu().numpy()).reshape(1).view(np.uint32), ref["g"].view(np.uint32))
+
+
+def test_jaxpr_emit_inside_a_cond_branch(cuda):
+    """the quickstart jaxpr with its emit inside a lax.cond branch (taken above x = 0.3): the histogram within the
+    float tolerance of the IR evaluator's, nothing in the bins below the gate, trip counts exact; the replay
+    gradient w.r.t. theta equal to that of the IR's own evaluation at theta +- h (the histogram is linear in theta)"""
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    fn, specs = FJ.item_function(J.quickstart(gate=0.3), ["hist"], 2)
+    f = tm.vmap(fn, outputs={"hist": tm.Sum((16,))}, in_axes=(0, 0, None), max_steps=100)
+    x, k = _inputs(10000)
+    r = f(x, k, np.float32(2.0))
+    torch.cuda.synchronize()
+    tr = T.trace_item(fn, specs, 2, {"hist": ((16,), "f32")})
+    ev = lambda th: Evaluator(tr, 100).run([x, k], [np.float32(th)])
+    ref = ev(2.0)
+    h = r.outputs["hist"].cpu().numpy().astype(np.float64)
+    assert np.abs(h - ref["sums"]["hist"]).max() <= 1e-5 * np.abs(ref["sums"]["hist"]).max()
+    assert h[:4].max() == 0.0 and np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
+    ct = np.random.default_rng(5).normal(size=16).astype(np.float32)
+    g = float(f.grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.from_numpy(ct)}))
+    want = float(np.dot(ct.astype(np.float64), (ev(2.5)["sums"]["hist"] - ev(1.5)["sums"]["hist"]) / 1.0))
+    assert abs(g - want) <= 1e-4 * abs(want)

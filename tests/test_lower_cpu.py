@@ -562,8 +562,8 @@ def test_special_math_trace_and_compile():
 
 
 def test_cond_switch_fori():
-    """lax.cond / switch of effect-free branches become selects (both traced, jax's semantics under vmap);
-    fori_loop with static bounds unrolls; a branch that writes the tally raises UnsupportedError"""
+    """lax.cond / switch of value branches become selects (both traced, jax's semantics under vmap);
+    fori_loop with static bounds unrolls; branches that use the tally differently raise TallyError"""
     from oracle.ir_eval import Evaluator
 
     def item(t, x, key, a):
@@ -584,9 +584,9 @@ def test_cond_switch_fori():
     assert np.array_equal(r["results"][2], z)
 
     def bad(t, x):
-        t = tl.cond(x > 0.5, lambda tt: tt.add("h", 0, 1.0), lambda tt: tt, t)
+        t, y = tl.cond(x > 0.5, lambda tt: (tt.add("h", 0, 1.0), x), lambda tt: (x, tt), t)
         return t
-    with pytest.raises(tm.UnsupportedError):
+    with pytest.raises(tm.TallyError, match="the same way"):
         T.trace_item(bad, ["f32"], 1, {"h": ((1,), "f32")})
     f = tm.vmap(item, outputs={"h": tm.Sum((1,))}, in_axes=(0, 0, None), max_steps=10)
     L = f.lowered((xs, prng.split(prng.PRNGKey(0), 4), np.float32(2.0)))
@@ -962,3 +962,44 @@ def test_records_argument_forms():
                 lambda: tm.Records({"a": tm.api.torch.float64}, 4), lambda: tm.Records({"a": f32}, fields={"b": f32})):
         with pytest.raises((TypeError, ValueError)):
             bad()
+
+
+def test_cond_branches_write_the_tally():
+    """t.add / t.append / t.spawn inside lax.cond and lax.switch branches (nested too) are made by the taken branch
+    only (tallymap/_rewrite.py:573-598): each effect carries its branch's predicate; the IR evaluator's sums, records
+    and results equal those of the same item written with selects, and the forward, reverse, forward-mode and
+    Records programs compile"""
+    from oracle.ir_eval import Evaluator
+    from items_lang import branch_writes, branch_writes_where, spawn_decay, spawn_decay_cond
+    n = 300
+    x = np.random.default_rng(3).uniform(0, 1, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(5), n)
+    specs = {"h": ((5,), "f32")}
+    recs = {"low": (1 << 14, (("k", "i32"), ("x", "f32")))}
+    tr = T.trace_item(branch_writes, ["f32", "key", "f32"], 2, specs, recs)
+    tw = T.trace_item(branch_writes_where, ["f32", "key", "f32"], 2, specs, recs)
+    emits = [e for e in tr.body if e.prim == "emit"]
+    assert len(emits) == 4 and all(len(e.ins) == 3 for e in emits)
+    assert [e for e in tr.body if e.prim == "append"][0].ins[0].dtype == T.BOOL
+    r = Evaluator(tr, 100).run([x, keys], [np.float32(1.3)])
+    w = Evaluator(tw, 100).run([x, keys], [np.float32(1.3)])
+    assert np.array_equal(r["sums"]["h"], w["sums"]["h"]) and r["sums"]["h"].min() > 0
+    assert r["records"]["low"] == w["records"]["low"] and len(r["records"]["low"]) > 0
+    assert np.array_equal(r["results"][0], w["results"][0])
+    f = tm.vmap(branch_writes, outputs={"h": tm.Sum((5,)), "low": tm.Records({"k": tm.api.torch.int32,
+                                                                        "x": tm.api.torch.float32})},
+                in_axes=(0, 0, None), max_steps=100)
+    L = f.lowered((x, keys, np.float32(1.3)))
+    assert L.fwd.kernel > 0 and L.grad_program((0,)).kernel > 0 and L.jvp_program((0,), 1).kernel > 0
+    assert all(p.kernel > 0 for p in L.records_programs())
+    src = lower.forward_source(L.it)[0]
+    assert src.count("if (v") >= 4
+    # a spawn inside a cond branch: the same tree as spawn_decay's `when`
+    g = np.zeros(50, np.int32)
+    wv = np.random.default_rng(1).uniform(0.5, 1.5, 50).astype(np.float32)
+    k2 = prng.split(prng.PRNGKey(13), 50)
+    specs = ["i32", "f32", "key", "f32"]
+    outs = {"Q": ((8,), "f32")}
+    ra, rb = (Evaluator(T.trace_item(fn, specs, 3, outs, spawn=True), 10).run([g, wv, k2], [np.float32(1.1)])
+              for fn in (spawn_decay_cond, spawn_decay))
+    assert np.array_equal(ra["sums"]["Q"], rb["sums"]["Q"]) and ra["stats"][0] == rb["stats"][0] == 100

@@ -935,3 +935,59 @@ def test_vector_results(cuda):
     assert np.array_equal(bits(xy[:, 0].cpu().numpy()), bits(ref["results"][0]))
     assert np.array_equal(bits(xy[:, 1].cpu().numpy()), bits(ref["results"][1]))
     assert np.array_equal(k.cpu().numpy(), ref["results"][2])
+
+
+def test_cond_branches_write_the_tally(cuda):
+    """t.add / t.append inside lax.cond / lax.switch branches (tallymap/_rewrite.py:573-598): the traced branch_writes
+    item against the IR evaluator (sums within the float tolerance, records and trip counts exact) and against the
+    same item written with selects (branch_writes_where) -- outputs, records, the reverse-mode gradient w.r.t. the
+    broadcast a and the per-item x, the one-pass value-and-grad and forward mode"""
+    from items_lang import branch_writes, branch_writes_where
+    n = 20000
+    x = np.random.default_rng(3).uniform(0, 1, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(5), n)
+    a = np.float32(1.3)
+    outs = {"h": tm.Sum((5,)), "low": tm.Records({"k": torch.int32, "x": torch.float32})}
+    fb = tm.vmap(branch_writes, outputs=outs, in_axes=(0, 0, None), max_steps=100)
+    fw = tm.vmap(branch_writes_where, outputs=outs, in_axes=(0, 0, None), max_steps=100)
+    rb, rw = fb(x, keys, a), fw(x, keys, a)
+    torch.cuda.synchronize()
+    recs = {"low": (1 << 20, (("k", "i32"), ("x", "f32")))}
+    ref = _eval(branch_writes, ["f32", "key", "f32"], 2, {"h": ((5,), "f32")}, recs, (x, keys, a), 100)
+    hb, hw = rb.outputs["h"].cpu().numpy(), rw.outputs["h"].cpu().numpy()
+    assert near(hb, ref["sums"]["h"]) and near(hb, hw)
+    assert np.array_equal(rb.per_item.cpu().numpy(), ref["results"][0])
+    m = len(ref["records"]["low"])
+    assert m > 0 and int(rb.stats["appended"]["low"]) == m
+    for j, fname in enumerate(("k", "x")):
+        got = rb.outputs["low"][fname].cpu().numpy()[:m]
+        assert np.array_equal(got, rw.outputs["low"][fname].cpu().numpy()[:m])
+        assert np.array_equal(got, np.array([r[j] for r in ref["records"]["low"]], got.dtype))
+    ct = {"h": torch.tensor([0.5, -1.0, 2.0, 1.5, -0.25])}
+    gb = fb.grad(x, keys, a, wrt=(0, 2), cotangents=ct)
+    gw = fw.grad(x, keys, a, wrt=(0, 2), cotangents=ct)
+    torch.cuda.synchronize()
+    assert near(gb[0].cpu().numpy(), gw[0].cpu().numpy(), 1e-6) and near(float(gb[1]), float(gw[1]), 1e-6)
+    assert float(gb[1]) != 0.0
+    _, vb = fb.value_and_grad(x, keys, a, wrt=2, cotangents=ct)
+    _, db = fb.jvp(x, keys, a, wrt=2, tangents=[1.0])
+    _, dw = fw.jvp(x, keys, a, wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    assert near(float(vb), float(gw[1]), 1e-5)
+    assert near(db["h"].cpu().numpy(), dw["h"].cpu().numpy(), 1e-6)
+
+
+def test_spawn_inside_a_cond_branch(cuda):
+    """a child spawned from inside a lax.cond branch: the same tree, outputs and tree-adjoint gradient as the
+    spawn's `when` gives (spawn_decay)"""
+    from items_lang import spawn_decay, spawn_decay_cond
+    args = _decay_args(3000)
+    ct = {"Q": torch.from_numpy(np.linspace(-1.0, 2.0, 8).astype(np.float32))}
+    res = []
+    for fn in (spawn_decay_cond, spawn_decay):
+        f = tm.vmap(fn, outputs={"Q": tm.Sum((8,))}, in_axes=(0, 0, 0, None), max_steps=10, spawn=tm.Queue(1 << 16))
+        r, (gw, ga) = f.value_and_grad(*args, np.float32(1.1), wrt=(1, 3), cotangents=ct)
+        torch.cuda.synchronize()
+        assert f.last_tree["children"] == 2 * 3000 and int(f.last_tree["mismatch"]) == 0
+        res.append((np_out(r)["Q"], gw.cpu().numpy(), float(ga)))
+    assert near(res[0][0], res[1][0]) and near(res[0][1], res[1][1], 1e-6) and near(res[0][2], res[1][2], 1e-6)
