@@ -8,8 +8,8 @@ How: `item_function` returns a Python item function fn(t, *leaves) that INTERPRE
 equation with this package's traced values (lang / trace), so tracing it (trace.trace_item, or tallymap_b200.vmap
 of it) records exactly the IR a hand-written item of the same program would.  Each equation is read through
 `eqn.primitive.name`, `eqn.params`, `eqn.invars` / `eqn.outvars` and each variable's `aval` (shape, dtype); a
-literal operand has `.val`; sub-jaxprs (`while`'s cond_jaxpr / body_jaxpr, `cond`'s branches, `pjit`'s jaxpr) are
-interpreted in place.  Nothing here imports JAX: any objects with those attributes work (the CPU tests use
+literal operand has `.val`; sub-jaxprs (`while`'s cond_jaxpr / body_jaxpr, `cond`'s branches, `scan`'s and `pjit`'s
+jaxpr) are interpreted in place.  Nothing here imports JAX: any objects with those attributes work (the CPU tests use
 duck-typed equation lists).
 
 Values: a scalar of shape () is a traced scalar or a numpy constant (equations whose operands are all constants are
@@ -21,7 +21,8 @@ output.  `tallymap_emit(t, idx, val)` becomes an emit at the flat index the refe
 The primitives read are those of jax.numpy / jax.random / lax on scalars and small vectors that the reference's
 op table lowers (op_table.py:47 RULES): arithmetic, comparisons, bitwise and shifts, select_n, clamp, conversions
 and bitcasts, the transcendentals, integer_pow, the random primitives (random_seed / wrap / unwrap / fold_in /
-bits / split, threefry2x32), while (the item's one top-level loop), cond, pjit and the call wrappers, shape
+bits / split, threefry2x32), while (the item's one top-level loop), cond (its branches' tally writes made only by
+the taken branch), scan of a static length (unrolled; jax's static fori_loop), pjit and the call wrappers, shape
 operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
 concatenate, iota, reductions).  Anything else raises UnsupportedError, as the reference's emitter does for a
 primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
@@ -268,6 +269,8 @@ class _Interp:
             return self.while_(e, a)
         if p == "cond":
             return self.cond(e, a)
+        if p == "scan":
+            return self.scan(e, a)
         if p == "tallymap_emit":
             ref, idx, val = a
             if not isinstance(ref, _TallyRef):
@@ -472,6 +475,32 @@ class _Interp:
             i = i.astype(tl.int32)
         r = tl.switch(i, fns, *[_py(x) for x in ops])
         return list(r) if isinstance(r, tuple) else [r]
+
+
+    def scan(self, e, a):
+        """lax.scan of a static length (and jax's fori_loop of static bounds, which it writes as a scan): unrolled
+        like tallymap_b200.lang.scan; the scanned inputs and stacked outputs are vectors of scalars (a tally may
+        ride in the carry: t.add inside the body)"""
+        prm = e.params
+        nc, nk, n = int(prm["num_consts"]), int(prm["num_carry"]), int(prm["length"])
+        if n > 4096:
+            raise T.UnsupportedError("tallymap_b200.from_jaxpr: a scan of more than 4096 steps (unrolled)")
+        consts, carry, xs = list(a[:nc]), list(a[nc:nc + nk]), list(a[nc + nk:])
+        for x in xs:
+            if not isinstance(x, T.Vec) or len(x) != n:
+                raise T.UnsupportedError("tallymap_b200.from_jaxpr: a scanned input that is not a vector of the "
+                                         "scan's length")
+        ny = len(e.outvars) - nk
+        ys = [[None] * n for _ in range(ny)]
+        for i in (range(n - 1, -1, -1) if prm.get("reverse") else range(n)):
+            out = self.call(prm["jaxpr"], consts + carry + [tuple.__getitem__(x, i) for x in xs])
+            carry = list(out[:nk])
+            for j, y in enumerate(out[nk:]):
+                if isinstance(y, (T.Vec, T.TallyToken)):
+                    raise T.UnsupportedError("tallymap_b200.from_jaxpr: a scan's stacked output is a vector of "
+                                             "scalars (per-item arrays have one dimension)")
+                ys[j][i] = y
+        return carry + [T.Vec(y) for y in ys]
 
 
 def _vec(f, x):

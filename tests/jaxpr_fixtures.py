@@ -153,6 +153,43 @@ def quickstart(cap=None, gate=None):
     return ClosedJaxpr(Jaxpr([hist, x0, key, theta], [oh] + results, eqns))
 
 
+def scans():
+    """a loop-free item with jax's two spellings of a static loop:
+
+        def item(t, x, key, theta):
+            c = lax.fori_loop(0, 3, lambda i, c: c * 0.5 + i, x)          # a scan carrying (i, c)
+            cs, ys = lax.scan(lambda c, z: (c + z * theta, c * z), 0.0, jnp.array([1.0, 2.0, 3.0]))
+            t = t.add("hist", 0, c).add("hist", 1, cs).add("hist", 2, ys[2])
+            return t, c
+    """
+    hist, x0, key, theta = Var(F, (16,)), Var(F), Var(U, (2,)), Var(F)
+    bi, bc, bi1, m, bf, bc1 = Var(I), Var(F), Var(I), Var(F), Var(F), Var(F)
+    b1 = ClosedJaxpr(Jaxpr([bi, bc], [bi1, bc1], [
+        Eqn("add", [bi, Literal(1, I)], [bi1]),
+        Eqn("mul", [bc, Literal(0.5, F)], [m]),
+        Eqn("convert_element_type", [bi], [bf], new_dtype="float32", weak_type=False),
+        Eqn("add", [m, bf], [bc1])]))
+    th, c, z, zt, c1, y = Var(F), Var(F), Var(F), Var(F), Var(F), Var(F)
+    b2 = ClosedJaxpr(Jaxpr([th, c, z], [c1, y], [
+        Eqn("mul", [z, th], [zt]),
+        Eqn("add", [c, zt], [c1]),
+        Eqn("mul", [c, z], [y])]))
+    i3, c3, cs, ys, y2s, y2, h1, h2, h3 = (Var(I), Var(F), Var(F), Var(F, (3,)), Var(F, (1,)), Var(F),
+                                           Var(F, (16,)), Var(F, (16,)), Var(F, (16,)))
+    zs = Literal(np.array([1.0, 2.0, 3.0], np.float32), F)
+    zs.aval = Aval((3,), F)
+    eqns = [Eqn("scan", [Literal(0, I), x0], [i3, c3], jaxpr=b1, length=3, reverse=False, num_consts=0,
+                num_carry=2, linear=(False, False), unroll=1),
+            Eqn("scan", [theta, Literal(0.0, F), zs], [cs, ys], jaxpr=b2, length=3, reverse=False, num_consts=1,
+                num_carry=1, linear=(False, False, False), unroll=1),
+            Eqn("slice", [ys], [y2s], start_indices=(2,), limit_indices=(3,), strides=None),
+            Eqn("squeeze", [y2s], [y2], dimensions=(0,)),
+            Eqn("tallymap_emit", [hist, Literal(0, I), c3], [h1]),
+            Eqn("tallymap_emit", [h1, Literal(1, I), cs], [h2]),
+            Eqn("tallymap_emit", [h2, Literal(2, I), y2], [h3])]
+    return ClosedJaxpr(Jaxpr([hist, x0, key, theta], [h3, c3], eqns))
+
+
 class TSpec:
     """the reference's TSpec, as ItemProgram.tallies holds them (tallymap/_api.py:204-220)"""
 

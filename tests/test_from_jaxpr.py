@@ -66,6 +66,32 @@ def test_emit_inside_a_cond_branch():
     assert r["sums"]["hist"][:4].max() == 0.0 and r["sums"]["hist"][5:].min() > 0.0
 
 
+def test_scan_and_static_fori_loop():
+    """jax's scan equation (lax.scan, and fori_loop of static bounds, which jax writes as a scan carrying the
+    counter) unrolls like tallymap_b200.lang's scan / fori_loop: the IR evaluator's outputs bitwise equal to the
+    same item written with lang"""
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import lang as tl
+    fn, specs = FJ.item_function(J.scans(), ["hist"], 2)
+    tr = T.trace_item(fn, specs, 2, SPECS)
+
+    def item(t, x, key, theta):
+        c = tl.fori_loop(0, 3, lambda i, c: c * 0.5 + float(i), x)
+        cs, ys = tl.scan(lambda c, z: (c + z * theta, c * z), 0.0, tl.array([1.0, 2.0, 3.0]))
+        t = t.add("hist", 0, c).add("hist", 1, cs).add("hist", 2, ys[2])
+        return t, c
+    x, k = _inputs(64)
+    r = Evaluator(tr, 10).run([x, k], [np.float32(1.5)])
+    rq = Evaluator(T.trace_item(item, ["f32", "key", "f32"], 2, SPECS), 10).run([x, k], [np.float32(1.5)])
+    assert np.array_equal(r["results"][0].view(np.uint32), rq["results"][0].view(np.uint32))
+    assert np.array_equal(r["sums"]["hist"].view(np.uint32), rq["sums"]["hist"].view(np.uint32))
+    c = x
+    for i in range(3):
+        c = (c * np.float32(0.5) + np.float32(i)).astype(np.float32)
+    assert np.array_equal(r["results"][0], c)
+    assert r["sums"]["hist"][1] == 64 * 9.0 and r["sums"]["hist"][2] == 64 * 13.5
+
+
 def test_retraced_program_carries_its_own_cap(orc):
     """the reference backend receives retrace(cap)'s program: its loop counter stops the loop and its own
     `truncated` is the second per-item result, equal to the oracle's flags at max_steps = 3"""

@@ -939,7 +939,7 @@ def test_vector_results(cuda):
 
 def test_cond_branches_write_the_tally(cuda):
     """t.add / t.append inside lax.cond / lax.switch branches (tallymap/_rewrite.py:573-598): the traced branch_writes
-    item against the IR evaluator (sums within the float tolerance, records and trip counts exact) and against the
+    item against the IR evaluator (fixed-point sums, records and trip counts bitwise) and against the
     same item written with selects (branch_writes_where) -- outputs, records, the reverse-mode gradient w.r.t. the
     broadcast a and the per-item x, the one-pass value-and-grad and forward mode"""
     from items_lang import branch_writes, branch_writes_where
@@ -947,15 +947,17 @@ def test_cond_branches_write_the_tally(cuda):
     x = np.random.default_rng(3).uniform(0, 1, n).astype(np.float32)
     keys = prng.split(prng.PRNGKey(5), n)
     a = np.float32(1.3)
-    outs = {"h": tm.Sum((5,)), "low": tm.Records({"k": torch.int32, "x": torch.float32})}
+    # (a fixed-point Sum: bin 1 sums a * a some 2e5 times, beyond what an f32 accumulation holds to 1e-5)
+    outs = {"h": tm.Sum((5,), fixed_point=True), "low": tm.Records({"k": torch.int32, "x": torch.float32})}
     fb = tm.vmap(branch_writes, outputs=outs, in_axes=(0, 0, None), max_steps=100)
     fw = tm.vmap(branch_writes_where, outputs=outs, in_axes=(0, 0, None), max_steps=100)
     rb, rw = fb(x, keys, a), fw(x, keys, a)
     torch.cuda.synchronize()
     recs = {"low": (1 << 20, (("k", "i32"), ("x", "f32")))}
-    ref = _eval(branch_writes, ["f32", "key", "f32"], 2, {"h": ((5,), "f32")}, recs, (x, keys, a), 100)
+    ref = _eval(branch_writes, ["f32", "key", "f32"], 2, {"h": ((5,), "f32")}, recs, (x, keys, a), 100,
+                exact=("h",))
     hb, hw = rb.outputs["h"].cpu().numpy(), rw.outputs["h"].cpu().numpy()
-    assert near(hb, ref["sums"]["h"]) and near(hb, hw)
+    assert np.array_equal(bits(hb), bits(ref["sums"]["h"])) and np.array_equal(bits(hb), bits(hw))
     assert np.array_equal(rb.per_item.cpu().numpy(), ref["results"][0])
     m = len(ref["records"]["low"])
     assert m > 0 and int(rb.stats["appended"]["low"]) == m
