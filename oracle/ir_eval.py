@@ -221,6 +221,12 @@ class Evaluator:
     def _run_eqns(self, eqns, env, out):
         for e in eqns:
             a = [self._val(x, env) for x in e.ins]
+            if e.prim == "claim":                  # (a Records slot claim: the launch's counter, in item order)
+                nm, c = e.params["tally"], self._claims.get(e.params["tally"], 0)
+                if a[0]:
+                    self._claims[nm] = c + 1
+                env[e.outs[0].id] = np.int32(c if a[0] and c < e.params["capacity"] else -1)
+                continue
             if e.prim == "emit":
                 if len(a) < 3 or a[2]:              # (a third operand: the predicate of a write in a cond branch)
                     out["emits"].append((e.params["tally"], a[0], a[1]))
@@ -242,6 +248,7 @@ class Evaluator:
 
     def run(self, per_item, bc):
         tr = self.tr
+        self._claims = {}
         n = len(per_item[0]) if per_item else 0
         specs = tr.specs
         sums = {}

@@ -84,6 +84,8 @@ class ItemProgram:
     records: tuple = ()             # Records outputs: ((name, capacity, ((field, torch dtype), ...)), ...)
     records_fill: bool = False      # the fill pass of count-then-fill: records go straight to their canonical slots
                                     # (offset + k from per-item operands), so the fields alone, sized by `capacity`
+    claims: int = 0                 # Records slot claims of a reference jaxpr (tallymap_claim): one u64 launch counter
+                                    # per tally (zeroed), after the Records buffers
 
     @property
     def n_args(self):
@@ -116,6 +118,8 @@ class ItemProgram:
             out.append((f"{name}#cid", cap * 4, torch.int32, (cap,)))
             out.append((f"{name}#k", cap * 4, torch.int32, (cap,)))
             out.append((f"{name}#ctr", 8, torch.int64, (1,)))
+        if self.claims:
+            out.append(("claims", 8 * self.claims, torch.int64, (self.claims,)))
         if self.queue_leaf_bytes:
             out.append(("queue.seq", max(queue, 1) * 4, torch.int32, (max(queue, 1),)))
             out.append(("queue.ctl", QCTL_WORDS * 4, torch.int32, (QCTL_WORDS,)))

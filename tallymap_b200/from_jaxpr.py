@@ -16,7 +16,9 @@ Values: a scalar of shape () is a traced scalar or a numpy constant (equations w
 folded in numpy with the aval's dtype, as XLA would fold them); a small 1-D array is a trace.Vec; a PRNG key
 (typed key<fry>, or uint32[2] key data under random_wrap) is a trace.Key; a tally array is a reference to its
 output.  `tallymap_emit(t, idx, val)` becomes an emit at the flat index the reference's Tally.add has formed
-(out-of-range indices dropped and counted, _tally.py:29-57); `tallymap_spawn(q, when, *leaves)` a spawn.
+(out-of-range indices dropped and counted, _tally.py:29-57); `tallymap_spawn(q, when, *leaves)` a spawn;
+`tallymap_claim(tok, when, k)` (a Records output's one-pass append, _tally.py:141-160, 335-351) a slot claim on the
+key tally `tok` (trace._claim), whose fields the jaxpr then emits at the slot.
 
 The primitives read are those of jax.numpy / jax.random / lax on scalars and small vectors that the reference's
 op table lowers (op_table.py:47 RULES): arithmetic, comparisons, bitwise and shifts, select_n, clamp, conversions
@@ -280,6 +282,13 @@ class _Interp:
             for i, v in zip(idxs, vals):
                 T._add_flat(self.tok, ref.name, _py(i), _py(v))
             return [ref]
+        if p == "tallymap_claim":
+            # (a Records output's one-pass append, tallymap/_tally.py:335-351: the slot, then its fields emitted
+            # there inside a cond on `ok`; the ordinal operand k is read only by the reference's fill twin)
+            ref, when = a[0], a[1]
+            if not isinstance(ref, _TallyRef):
+                raise T.TraceError("tallymap_b200.from_jaxpr: a claim on something other than a tally")
+            return [ref, T._claim(self.tok, ref.name, _py(when))]
         if p == "tallymap_spawn":
             q, when, *leaves = a
             self.tok.spawn(tuple(_py(x) for x in leaves), when=_py(when))

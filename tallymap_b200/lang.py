@@ -268,7 +268,7 @@ def _branch_select(picks, results):
     return rebuild(out)
 
 
-_EFFECTS = ("emit", "append", "spawn")
+_EFFECTS = ("emit", "append", "spawn", "claim")     # (claim: a Records slot claim of the jaxpr front end)
 
 
 class _Pick:

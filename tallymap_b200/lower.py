@@ -272,6 +272,10 @@ class Item:
         self.post_spawns = any(e.prim == "spawn" for e in tr.post)
         if self.spawns and tr.records:
             raise NotImplementedError("tallymap_b200: Records outputs of a spawning item are not lowered")
+        # Records slot claims of the jaxpr front end: one launch counter per claimed tally (by its output position)
+        self.claims = any(e.prim == "claim" for e in tr.pre + tr.body + tr.post)
+        if self.claims and self.spawns:
+            raise NotImplementedError("tallymap_b200: Records slot claims in a spawning item are not lowered")
         # step counters: carries that start at 0 and gain 1 per step equal the step index (not stored by the replay)
         self.counter = set()
         by_id = {o.id: e for e in tr.body for o in e.outs}
@@ -359,7 +363,7 @@ def _spawn_record_code(it, gen, last):
     return spawner
 
 
-def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None, spawner=None):
+def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=None, spawner=None, claimer=None):
     """straight-line C for eqns; names: id -> C expression (updated with the locals defined here)"""
     out = []
     for e in eqns:
@@ -371,6 +375,13 @@ def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=N
         if e.prim == "append":
             if appender is not None:
                 out.append(indent + appender(e.params["records"], a[0], a[1:]))
+            continue
+        if e.prim == "claim":
+            if claimer is None:
+                raise LowerError("tallymap_b200.lower: a Records slot claim (tallymap_claim) lowers in the forward "
+                                 "program only: the reference's derived programs run its fill twin")
+            out.append(indent + claimer(e, a[0]))
+            names[e.outs[0].id] = f"v{e.outs[0].id}"
             continue
         if e.prim == "emit":
             if not skip_emits:
@@ -440,6 +451,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
         enum.append(f"kR{r}Cid = {idx}"); idx += 1
         enum.append(f"kR{r}K = {idx}"); idx += 1
         enum.append(f"kR{r}Ctr = {idx}"); idx += 1
+    if it.claims:
+        enum.append(f"kClaims = {idx}"); idx += 1
     if sp:
         enum.append(f"kSeq = {idx}"); idx += 1
         enum.append(f"kQctl = {idx}"); idx += 1
@@ -514,6 +527,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
         ctx.append(f"    i32* r{r}n;")
     if recs:
         ctx.append("    i64 item;")
+    if it.claims:
+        ctx.append("    unsigned long long* claims;   // per tally: its Records slot counter")
     if rec:
         ctx += ["    i32* rec;", "    unsigned short* rgen;", "    unsigned long long* tree;", "    i32* lastout;",
                 "    u64 R;"]
@@ -560,6 +575,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
             lines += [f"    c.rcnt{r} = static_cast<const i32*>(P.p[kRCnt{r}]);",
                       f"    c.roff{r} = static_cast<const long long*>(P.p[kROff{r}]);"]
         lines.append(f"    c.r{r}n = static_cast<i32*>(P.p[kR{r}N]);")
+    if it.claims:
+        lines.append("    c.claims = static_cast<unsigned long long*>(P.p[kClaims]);")
     if rec:
         lines += ["    c.rec = static_cast<i32*>(P.p[kRecord]);",
                   "    c.rgen = static_cast<unsigned short*>(P.p[kRecGen]);",
@@ -594,6 +611,13 @@ def forward_source(it, standalone=True, record=False, mode="one"):
             return "".join(st)
         return appender
 
+    def claimer(e, when_c):
+        """a Records slot claim (tallymap/backends/kernel/kernel.py:1052-1070): the next slot of the claimed
+        tally's raw buffer, one atomic on its launch counter; -1 when not `when` or past the capacity"""
+        o, t = e.outs[0].id, tinfo[e.params["tally"]][0]
+        return (f"i32 v{o} = -1; if ({when_c}) {{ const unsigned long long o_ = atomicAdd(&c.claims[{t}], 1ull); "
+                f"if (o_ < {int(e.params['capacity'])}ull) v{o} = (i32)o_; }}")
+
     def emitter(name, idx_c, v_c):
         t, S, dt, pv = tinfo[name]
         if name in it.exact:
@@ -623,7 +647,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
                 lines += [f"    c.rn{r} = __ldg(&c.rcnt{r}[item]); c.ro{r} = __ldg(&c.roff{r}[item]);"
                           for r in range(len(recs))]
         lines += _emit_code(tr.pre, names, emitter, appender=appender_for(lambda r: f"a{r}") if recs else None,
-                            skip_emits=count)
+                            skip_emits=count, claimer=claimer)
         for i in it.saved:
             lines.append(f"    c.p{i} = {names[i]};")
         lines.append("    State s;")
@@ -651,7 +675,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
         names = _names_loop(it, tr.carry)
         for i in live:
             names[i] = f"d.d{i}"
-        lines += _emit_code(rest, names, emitter)
+        lines += _emit_code(rest, names, emitter, claimer=claimer)
         lines += _assign_carry(it, names)
         lines.append("  }")
         lines.append("  __device__ __forceinline__ static void step(const Ctx& c, State& s) { apply(c, s, draw(c, s, 0)); }")
@@ -682,7 +706,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
         names = _names_loop(it, tr.carry)
         lines += _emit_code(tr.body, names, emitter, appender=appender_for(lambda r: f"s.a{r}"),
                             spawner=_spawn_record_code(it, "s.gen", "s.last") if rec else _spawn_code,
-                            skip_emits=count)
+                            skip_emits=count, claimer=claimer)
         lines += _assign_carry(it, names)
         lines.append("  }")
     if not sp:
@@ -698,7 +722,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     if rec:
         lines.append("    i32 last_ = s.last;")
     lines += _emit_code(tr.post, names, emitter, appender=appender_for(lambda r: f"a{r}"),
-                        spawner=_spawn_record_code(it, "s.gen", "last_") if rec else _spawn_code, skip_emits=count)
+                        spawner=_spawn_record_code(it, "s.gen", "last_") if rec else _spawn_code, skip_emits=count,
+                        claimer=claimer)
     if sp:
         # a child's per-item results are discarded (tallymap/_tally.py:285-286); its truncation is counted
         lines.append("    const bool tr_ = s.kc >= c.M && pred(c, s);")
@@ -778,7 +803,7 @@ def _draw_split(it):
     fixed = set(it.saved) | set(it.bc_ids) | {tr.carry[j].id for j in it.counter}
     draws, rest, dset = [], [], set()
     for e in tr.body:
-        ok = e.prim not in ("emit", "spawn", "append") and \
+        ok = e.prim not in ("emit", "spawn", "append", "claim") and \
             all(not isinstance(x, T.Var) or x.id in fixed or x.id in dset for x in e.ins)
         if ok:
             draws.append(e)
@@ -1538,7 +1563,8 @@ class Lowered:
         records = tuple((nm, int(cap), tuple((f, TDTYPE[dt]) for f, dt in fl)) for nm, (cap, fl) in recs.items())
         nrec = sum(len(fl) + 3 for _, _, fl in records)
         sp = it.spawns
-        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys) + (3 if sp else 0)
+        nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys) + (3 if sp else 0) + \
+            int(it.claims)
         if sp:
             # the spawn runtime's shared stack entries after the item's block (csrc/tm_spawn.cuh SpawnSmem)
             smem = (smem + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * len(it.loads) * 128
@@ -1547,7 +1573,8 @@ class Lowered:
         self.fwd = ItemProgram(self.name + "_fwd", kid, pi=pi, bc=bc,
                                consts=("max_steps", "queue") if sp else ("max_steps",), tallies=tallies,
                                ys=ys, trunc=len(ys) - 1, records=records, spawns=sp,
-                               queue_leaf_bytes=4 * len(it.loads) if sp else 0)
+                               queue_leaf_bytes=4 * len(it.loads) if sp else 0,
+                               claims=len(tallies) if it.claims else 0)
         self.n_results = len(self.tr.results)
         self._fwd_nbuf = nbuf
         self.grads = {}

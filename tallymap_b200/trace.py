@@ -521,6 +521,24 @@ def _add_flat(tok, name, flat, value):
     return tok
 
 
+def _claim(tok, name, when):
+    """a Records output's one-pass slot claim as the reference's jaxprs hold it (tallymap/_tally.py:141-160
+    claim_p, its kernel rule backends/kernel/kernel.py:1052-1070): the next slot of the raw buffer behind the int32
+    Sum `name` (its capacity = the tally's size) from a per-launch counter, or -1 when `when` is false or the buffer
+    is full (the counter still counts: it holds the true total).  The jaxpr front end's `tallymap_claim`; the fields
+    are then ordinary emits at the slot.  -> the slot, an int32"""
+    if name not in tok.specs:
+        raise TraceError(f"tallymap_b200: a claim on {name!r}, which is not a tally")
+    shape, dt = tok.specs[name]
+    w = _lit(when)
+    if w.dtype != BOOL:
+        raise TraceError("tallymap_b200: a claim's `when` must be a scalar bool")
+    cap = 1
+    for d in shape:
+        cap *= int(d)
+    return _cur().emit("claim", [w], [I32], tally=name, capacity=cap)[0]
+
+
 def _flat_index(index, shape):
     """row-major flat index; any coordinate outside its dimension gives -1 (_tally.py:260-271)"""
     if not isinstance(index, tuple):

@@ -514,3 +514,16 @@ def spawn_decay_cond(t, g, w, key, a):
     k, w, t = tl.while_loop(lambda c: c[0] < 3, body, (0, w, t))
     t = tl.cond(g < 2, lambda tt: tt.spawn((g + 1, w * a, tl.random.fold_in(key, 7))), lambda tt: tt, t)
     return t, k
+
+
+def quickstart_hits(t, x, key, theta):
+    """the quickstart walker appending {"x": x} at each step that starts in bin 3 (a Records output "hits")"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        b = (x * 16).astype(tl.int32)
+        t = t.add("hist", b, theta * (1 - x))
+        t = t.append("hits", {"x": x}, when=b == 3)
+        return k + 1, x * (0.5 + 0.5 * u), t
+    k, x, t = tl.while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
+    return t, k

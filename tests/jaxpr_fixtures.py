@@ -190,6 +190,72 @@ def scans():
     return ClosedJaxpr(Jaxpr([hist, x0, key, theta], [h3, c3], eqns))
 
 
+RSEP = "\x1f"
+
+
+def quickstart_records(C=4096):
+    """the quickstart walker with a Records output in the reference's ONE-PASS form (tallymap/_tally.py:302-351,
+    _api.py:727-733): each step that starts in bin 3 appends {"x": x}.  The item's tallies are hist, then the record
+    field tally 'hits\x1fx' and the key tallies 'hits\x1fi' (the item's node id) and 'hits\x1fk' (its ordinal),
+    each of the capacity C; the per-item operands end with the hidden node id (arange(N)); the append ordinal rides
+    in the carry and is the second per-item result (the item's count).  Per append:
+
+        tok, slot = tallymap_claim(t['hits\x1fk'], w, k, r=0)
+        ok = w & (slot >= 0) & (slot < C)
+        (hx, hi, hk) = lax.cond(ok, put1, lambda ts: ts, (t['hits\x1fx'], t['hits\x1fi'], tok))
+        k = k + w
+    """
+    hist, hx, hki, hkk = Var(F, (16,)), Var(F, (C,)), Var(I, (C,)), Var(I, (C,))
+    x0, key, cid, theta = Var(F), Var(U, (2,)), Var(I), Var(F)
+    bkey, btheta, bcid = Var(U, (2,)), Var(F), Var(I)
+    bk, bx, bh, bhx, bhi, bhk, bkr = Var(I), Var(F), Var(F, (16,)), Var(F, (C,)), Var(I, (C,)), Var(I, (C,)), Var(I)
+    m, ku, n, o, p = Var(KEY), Var(U), Var(KEY), Var(U, (2,)), Var(F)
+    be, bf, bg, bh2, bi, bj, bk2, bl, bm = Var(F), Var(I), Var(F), Var(F), Var(F, (16,)), Var(I), Var(F), Var(F), Var(F)
+    w, tk, slot, s0, s1, ok0, ok, oi = Var(B), Var(I, (C,)), Var(I), Var(B), Var(B), Var(B), Var(B), Var(I)
+    hx2, hi2, hk2, wi, kr2 = Var(F, (C,)), Var(I, (C,)), Var(I, (C,)), Var(I), Var(I)
+    # the branches: (slot, x, cid, k, field tally, key tallies) -> the three tallies
+    ids = [Var(I), Var(F), Var(I), Var(I), Var(F, (C,)), Var(I, (C,)), Var(I, (C,))]
+    put = [Var(I), Var(F), Var(I), Var(I), Var(F, (C,)), Var(I, (C,)), Var(I, (C,))]
+    pa, pb, pc = Var(F, (C,)), Var(I, (C,)), Var(I, (C,))
+    identity = ClosedJaxpr(Jaxpr(ids, ids[4:], []))
+    put1 = ClosedJaxpr(Jaxpr(put, [pa, pb, pc], [Eqn("tallymap_emit", [put[4], put[0], put[1]], [pa]),
+                                                 Eqn("tallymap_emit", [put[5], put[0], put[2]], [pb]),
+                                                 Eqn("tallymap_emit", [put[6], put[0], put[3]], [pc])]))
+    body_eqns = [Eqn("random_wrap", [bkey], [m], impl="fry"),
+                 Eqn("convert_element_type", [bk], [ku], new_dtype="uint32", weak_type=False),
+                 Eqn("random_fold_in", [m, ku], [n]),
+                 Eqn("random_unwrap", [n], [o]),
+                 Eqn("pjit", [o, Literal(0.0, F), Literal(1.0, F)], [p], jaxpr=uniform_pjit(), name="_uniform"),
+                 Eqn("mul", [bx, Literal(16.0, F)], [be]),
+                 Eqn("convert_element_type", [be], [bf], new_dtype="int32", weak_type=False),
+                 Eqn("sub", [Literal(1.0, F), bx], [bg]),
+                 Eqn("mul", [btheta, bg], [bh2]),
+                 Eqn("tallymap_emit", [bh, bf, bh2], [bi]),
+                 Eqn("eq", [bf, Literal(3, I)], [w]),
+                 Eqn("tallymap_claim", [bhk, w, bkr], [tk, slot], r=0),
+                 Eqn("ge", [slot, Literal(0, I)], [s0]),
+                 Eqn("lt", [slot, Literal(C, I)], [s1]),
+                 Eqn("and", [w, s0], [ok0]),
+                 Eqn("and", [ok0, s1], [ok]),
+                 Eqn("convert_element_type", [ok], [oi], new_dtype="int32", weak_type=False),
+                 Eqn("cond", [oi, slot, bx, bcid, bkr, bhx, bhi, tk], [hx2, hi2, hk2], branches=(identity, put1)),
+                 Eqn("convert_element_type", [w], [wi], new_dtype="int32", weak_type=False),
+                 Eqn("add", [bkr, wi], [kr2]),
+                 Eqn("add", [bk, Literal(1, I)], [bj]),
+                 Eqn("mul", [Literal(0.5, F), p], [bk2]),
+                 Eqn("add", [Literal(0.5, F), bk2], [bl]),
+                 Eqn("mul", [bx, bl], [bm])]
+    body = ClosedJaxpr(Jaxpr([bkey, btheta, bcid, bk, bx, bh, bhx, bhi, bhk, bkr],
+                             [bj, bm, bi, hx2, hi2, hk2, kr2], body_eqns))
+    ck, cx, ch, chx, chi, chk, ckr, cq = (Var(I), Var(F), Var(F, (16,)), Var(F, (C,)), Var(I, (C,)), Var(I, (C,)),
+                                          Var(I), Var(B))
+    cond = ClosedJaxpr(Jaxpr([ck, cx, ch, chx, chi, chk, ckr], [cq], [Eqn("gt", [cx, Literal(0.05, F)], [cq])]))
+    ok_, ox, oh, ohx, ohi, ohk, okr = Var(I), Var(F), Var(F, (16,)), Var(F, (C,)), Var(I, (C,)), Var(I, (C,)), Var(I)
+    eqns = [Eqn("while", [key, theta, cid, Literal(0, I), x0, hist, hx, hki, hkk, Literal(0, I)],
+                [ok_, ox, oh, ohx, ohi, ohk, okr], cond_jaxpr=cond, body_jaxpr=body, cond_nconsts=0, body_nconsts=3)]
+    return ClosedJaxpr(Jaxpr([hist, hx, hki, hkk, x0, key, cid, theta], [oh, ohx, ohi, ohk, ok_, okr], eqns))
+
+
 class TSpec:
     """the reference's TSpec, as ItemProgram.tallies holds them (tallymap/_api.py:204-220)"""
 
@@ -204,6 +270,14 @@ class ItemProgram:
     def __init__(self, cj, tallies, nP, nB, trunc=None, spawn=None):
         self.cj, self.tallies, self.nP, self.nB, self.trunc, self.spawn = cj, tuple(tallies), nP, nB, trunc, spawn
         self.tag = "primal"
+
+
+def records_program(C=4096):
+    """the one-pass Records quickstart as the reference's backend entry receives it (no retrace cap: the loop ends on
+    its own)"""
+    return ItemProgram(quickstart_records(C), [TSpec("hist", 16), TSpec("hits" + RSEP + "x", C),
+                                               TSpec("hits" + RSEP + "i", C, "int32"),
+                                               TSpec("hits" + RSEP + "k", C, "int32")], nP=3, nB=1)
 
 
 def quickstart_program(cap=100):

@@ -92,6 +92,48 @@ def test_scan_and_static_fori_loop():
     assert r["sums"]["hist"][1] == 64 * 9.0 and r["sums"]["hist"][2] == 64 * 13.5
 
 
+def test_records_one_pass_claims():
+    """the reference's one-pass Records append in a jaxpr (tallymap_claim, then the field, the node id and the
+    ordinal emitted at the claimed slot inside a cond; tallymap/_tally.py:335-351): with the items run in order (the
+    IR evaluator) the raw slots are the canonical layout, the records of the same item written with lang's
+    t.append; the forward program compiles with one slot counter per tally, and a derived program refuses the claim
+    (the reference runs its fill twin there)"""
+    from oracle.ir_eval import Evaluator
+    import tallymap_b200 as tm
+    import torch
+    from items_lang import quickstart_hits
+    C = 4096
+    names = ["hist", "hits\x1fx", "hits\x1fi", "hits\x1fk"]
+    fn, specs = FJ.item_function(J.quickstart_records(C), names, 3)
+    assert specs == ["f32", "key", "i32", "f32"]
+    sp = {"hist": ((16,), "f32"), names[1]: ((C,), "f32"), names[2]: ((C,), "i32"), names[3]: ((C,), "i32")}
+    tr = T.trace_item(fn, specs, 3, sp)
+    assert sum(e.prim == "claim" for e in tr.body) == 1
+    assert sum(e.prim == "emit" and len(e.ins) == 3 for e in tr.body) == 3
+    n = 3000
+    x, k = _inputs(n)
+    cid = np.arange(n, dtype=np.int32)
+    r = Evaluator(tr, 100).run([x, k, cid], [2.0])
+    tq = T.trace_item(quickstart_hits, ["f32", "key", "f32"], 2, SPECS, {"hits": (C, (("x", "f32"),))})
+    rq = Evaluator(tq, 100).run([x, k], [2.0])
+    cnt = rq["counts"]["hits"]
+    m = len(rq["records"]["hits"])
+    assert 0 < m < C and np.array_equal(r["results"][1], cnt)
+    assert np.array_equal(r["results"][0], rq["results"][0]) and np.array_equal(r["sums"]["hist"], rq["sums"]["hist"])
+    want = np.array([v[0] for v in rq["records"]["hits"]], np.float32)
+    assert np.array_equal(r["sums"][names[1]][:m].astype(np.float32).view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(r["sums"][names[2]][:m], np.repeat(np.arange(n), cnt))
+    assert np.array_equal(r["sums"][names[3]][:m], np.concatenate([np.arange(c) for c in cnt]))
+    assert not r["sums"][names[1]][m:].any()
+    outs = {"hist": tm.Sum((16,)), names[1]: tm.Sum((C,)), names[2]: tm.Sum((C,), torch.int32),
+            names[3]: tm.Sum((C,), torch.int32)}
+    f = tm.vmap(fn, outputs=outs, in_axes=(0, 0, 0, None), max_steps=100)
+    L = f.lowered((x[:8], k[:8], cid[:8], np.float32(2.0)))
+    assert L.fwd.kernel > 0 and L.fwd.claims == 4 and "atomicAdd(&c.claims[3], 1ull)" in L.fwd_source
+    with pytest.raises(T.UnsupportedError, match="fill twin"):
+        L.grad_program((0,))
+
+
 def test_retraced_program_carries_its_own_cap(orc):
     """the reference backend receives retrace(cap)'s program: its loop counter stops the loop and its own
     `truncated` is the second per-item result, equal to the oracle's flags at max_steps = 3"""

@@ -64,3 +64,36 @@ def test_jaxpr_emit_inside_a_cond_branch(cuda):
     g = float(f.grad(x, k, np.float32(2.0), wrt=2, cotangents={"hist": torch.from_numpy(ct)}))
     want = float(np.dot(ct.astype(np.float64), (ev(2.5)["sums"]["hist"] - ev(1.5)["sums"]["hist"]) / 1.0))
     assert abs(g - want) <= 1e-4 * abs(want)
+
+
+@pytest.mark.parametrize("C", [1 << 15, 64])
+def test_reference_records_program_runs(cuda, C):
+    """the reference's one-pass Records program (tallymap_claim + the cond that writes the claimed slot) through
+    run(): every raw slot below min(total, C) holds one record, whose (node id, ordinal) key places it at the
+    canonical slot (tallymap/_records.py:35-62 canon) with the field the IR evaluator gives that record, bitwise;
+    the counts (per-item results) and trip counts exact; a capacity below the total keeps C of the records and
+    drops no other write"""
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    from items_lang import quickstart_hits
+    n = 10000
+    x, k = _inputs(n)
+    cid = np.arange(n, dtype=np.int32)
+    out = FJ.run(J.records_program(C), [x, k, cid], [np.float32(2.0)], target="cuda", cuda_math="ieee")
+    torch.cuda.synchronize()
+    hist, hx, hi, hk, stats, kk, cnt = [o.cpu().numpy() for o in out]
+    tq = T.trace_item(quickstart_hits, ["f32", "key", "f32"], 2, {"hist": ((16,), "f32")},
+                      {"hits": (1 << 20, (("x", "f32"),))})
+    ref = Evaluator(tq, 100).run([x, k], [np.float32(2.0)])
+    want_cnt = ref["counts"]["hits"]
+    total = int(want_cnt.sum())
+    assert np.array_equal(cnt, want_cnt) and np.array_equal(kk, ref["results"][0]) and not stats.any()
+    assert np.abs(hist - ref["sums"]["hist"]).max() <= 1e-5 * np.abs(ref["sums"]["hist"]).max()
+    want_x = np.array([v[0] for v in ref["records"]["hits"]], np.float32)
+    off = np.concatenate([[0], np.cumsum(want_cnt)[:-1]])
+    m = min(total, C)
+    assert total > 0 and (C > total or total > 2 * C)
+    pos = off[hi[:m]] + hk[:m]
+    assert (hk[:m] < want_cnt[hi[:m]]).all() and len(np.unique(pos)) == m
+    assert np.array_equal(hx[:m].view(np.uint32), want_x[pos].view(np.uint32))
+    assert not hx[m:].any() and not hi[m:].any() and not hk[m:].any()
