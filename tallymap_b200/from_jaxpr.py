@@ -26,7 +26,9 @@ and bitcasts, the transcendentals, integer_pow, the random primitives (random_se
 bits / split, threefry2x32), while (the item's one top-level loop), cond (its branches' tally writes made only by
 the taken branch), scan of a static length (unrolled; jax's static fori_loop), pjit and the call wrappers, shape
 operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
-concatenate, iota, reductions).  Anything else raises UnsupportedError, as the reference's emitter does for a
+dynamic_update_slice, concatenate, pad, rev, iota, reductions, cumsum / cumprod / cummax / cummin, dot_general with
+a result of at most one dimension), jit (jax >= 0.7's name for pjit), random_clone / random_key_data,
+iota_2x32_shape and platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a
 primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
 
 `run(p, pi, bc, target, cuda_math, schedule, ndev, min_blocks_per_sm)` is the reference's backend entry
@@ -260,8 +262,11 @@ class _Interp:
         idt = _dtype(e.invars[0].aval) if e.invars and not _is_key(e.invars[0].aval) else None
 
         # calls: interpreted in place
-        if p in ("pjit", "closed_call", "core_call", "remat", "checkpoint", "custom_jvp_call", "custom_vjp_call",
-                 "custom_vjp_call_jaxpr", "custom_lin"):
+        if p == "custom_lin":
+            raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: custom_lin (a linearized custom_vjp) is not lowered "
+                                       "inside an item, as the reference's kernel backend refuses it")
+        if p in ("pjit", "jit", "closed_call", "core_call", "remat", "remat2", "checkpoint", "custom_jvp_call",
+                 "custom_vjp_call", "custom_vjp_call_jaxpr"):
             sub = prm.get("jaxpr") or prm.get("call_jaxpr") or prm.get("fun_jaxpr")
             if sub is None:
                 raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} without a jaxpr")
@@ -338,6 +343,30 @@ class _Interp:
             f = {"reduce_sum": tl.sum, "reduce_max": tl.max, "reduce_min": tl.min, "reduce_and": tl.all,
                  "reduce_or": tl.any, "argmax": tl.argmax, "argmin": tl.argmin}[p]
             return [f(_py(x))]
+
+        if p == "rev":
+            (x,) = a
+            return [T.Vec(reversed(list(x))) if isinstance(x, T.Vec) else x]
+        if p == "transpose":
+            if tuple(prm.get("permutation", ())) not in ((), (0,)):
+                raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: transpose of more than one dimension")
+            return [a[0]]
+        if p == "pad":
+            return [_pad(a[0], a[1], prm["padding_config"])]
+        if p in _CUM:
+            return [_cumulative(p, a[0], bool(prm.get("reverse", False)), odt)]
+        if p == "dot_general":
+            return [_dot_general(e, a[0], a[1], prm["dimension_numbers"], odt)]
+        if p == "dynamic_update_slice":
+            return [_dynamic_update_slice(a[0], a[1], a[2] if len(a) > 2 else np.int32(0))]
+        if p == "iota_2x32_shape":
+            shape = tuple(int(d) for d in prm["shape"])
+            n = int(np.prod(shape, dtype=np.int64)) if shape else 1
+            if shape == ():
+                return [np.uint32(0), np.uint32(0)]
+            return [T.Vec([np.uint32(0)] * n), T.Vec(np.uint32(i) for i in range(n))]
+        if p == "platform_index":
+            return [np.int32(_platform_index(prm["platforms"]))]
 
         # elementwise
         if p == "select_n":
@@ -512,6 +541,121 @@ class _Interp:
         return carry + [T.Vec(y) for y in ys]
 
 
+_CUM = {"cumsum": (np.add, lambda u, w: u + w), "cumprod": (np.multiply, lambda u, w: u * w),
+        "cummax": (np.maximum, tl.maximum), "cummin": (np.minimum, tl.minimum)}
+
+
+def _arith(f_np, f_tl, u, w, dt=None):
+    """one binary step on constants (numpy, in the operands' dtype) or traced values"""
+    if isinstance(u, np.generic) and isinstance(w, np.generic):
+        with np.errstate(all="ignore"):
+            r = f_np(u, w)
+        return _NP[dt](r) if dt is not None else r
+    return f_tl(_py(u), _py(w))
+
+
+def _cumulative(p, x, reverse, dt):
+    """lax.cumsum / cumprod / cummax / cummin of a vector: the running value element by element, from the last
+    element when reverse (the reference's sequential loop, backends/kernel/op_table.py:930-961)"""
+    xs = list(x) if isinstance(x, T.Vec) else [x]
+    f_np, f_tl = _CUM[p]
+    out, acc = [None] * len(xs), None
+    for i in (range(len(xs) - 1, -1, -1) if reverse else range(len(xs))):
+        acc = xs[i] if acc is None else _arith(f_np, f_tl, acc, xs[i], dt)
+        out[i] = acc
+    return T.Vec(out)
+
+
+def _pad(x, v, config):
+    """lax.pad of a vector by padding_config ((lo, hi, interior),): interior copies of v between elements, then lo /
+    hi copies at the ends (a negative lo / hi crops)"""
+    ((lo, hi, interior),) = [tuple(int(c) for c in cfg) for cfg in config]
+    xs = list(x) if isinstance(x, T.Vec) else [x]
+    out = []
+    for i, y in enumerate(xs):
+        if i:
+            out += [v] * interior
+        out.append(y)
+    out = [v] * max(lo, 0) + out[max(-lo, 0):]
+    out = out + [v] * max(hi, 0) if hi >= 0 else out[:len(out) + hi]
+    return T.Vec(out)
+
+
+def _dot_general(e, x, y, dimension_numbers, dt):
+    """lax.dot_general over row-major flattened operands (their shapes from the avals): per output element, a sum
+    from the literal zero in contraction order, acc = acc + x * y with no fused multiply-add (the reference's rule,
+    backends/kernel/op_table.py:964-1003)"""
+    (lc, rc), (lb, rb) = dimension_numbers
+    ls, rs = tuple(e.invars[0].aval.shape), tuple(e.invars[1].aval.shape)
+    xs = list(x) if isinstance(x, T.Vec) else [x]
+    ys = list(y) if isinstance(y, T.Vec) else [y]
+    lf = [d for d in range(len(ls)) if d not in lc and d not in lb]
+    rf = [d for d in range(len(rs)) if d not in rc and d not in rb]
+    bshape = tuple(ls[d] for d in lb)
+    cshape = tuple(ls[d] for d in lc)
+    oshape = bshape + tuple(ls[d] for d in lf) + tuple(rs[d] for d in rf)
+    if len(oshape) > 1:
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a dot_general whose result has more than one dimension")
+    out = []
+    for oidx in np.ndindex(*oshape):
+        bi, li_, ri_ = oidx[:len(lb)], oidx[len(lb):len(lb) + len(lf)], oidx[len(lb) + len(lf):]
+        acc = _NP[dt](0)
+        for cidx in np.ndindex(*cshape):
+            li, ri = [0] * len(ls), [0] * len(rs)
+            for j, d in enumerate(lb):
+                li[d] = bi[j]
+            for j, d in enumerate(rb):
+                ri[d] = bi[j]
+            for j, d in enumerate(lf):
+                li[d] = li_[j]
+            for j, d in enumerate(rf):
+                ri[d] = ri_[j]
+            for j, (dl, dr) in enumerate(zip(lc, rc)):
+                li[dl] = cidx[j]
+                ri[dr] = cidx[j]
+            u = xs[int(np.ravel_multi_index(li, ls))] if ls else xs[0]
+            w = ys[int(np.ravel_multi_index(ri, rs))] if rs else ys[0]
+            acc = _arith(np.add, lambda s_, t_: s_ + t_, acc, _arith(np.multiply, lambda s_, t_: s_ * t_, u, w, dt), dt)
+        out.append(acc)
+    return out[0] if oshape == () else T.Vec(out)
+
+
+def _dynamic_update_slice(x, upd, start):
+    """lax.dynamic_update_slice of a vector: the update written from the start index clamped so that it fits; a
+    traced start selects per element"""
+    xs = list(x) if isinstance(x, T.Vec) else [x]
+    us = list(upd) if isinstance(upd, T.Vec) else [upd]
+    n, m = len(xs), len(us)
+    if isinstance(start, T.Vec):
+        start = tuple.__getitem__(start, 0)
+    if isinstance(start, (np.generic, int)):
+        s = int(np.clip(int(start), 0, n - m))
+        return T.Vec(xs[:s] + us + xs[s + m:])
+    s = tl.clip(_py(start), 0, n - m)
+    out = []
+    for j in range(n):
+        r = _py(xs[j])
+        for i in range(m):
+            if 0 <= j - i <= n - m:
+                r = tl.where(s == j - i, _py(us[i]), r)
+        out.append(r)
+    return T.Vec(out)
+
+
+def _platform_index(platforms):
+    """lax.platform_dependent's branch index for a CUDA device: the branch naming cuda / gpu, else the default
+    (the reference's rule, backends/kernel/op_table.py:1650-1659)"""
+    plats = list(platforms)
+    for i, ps in enumerate(plats):
+        if ps is not None and any(x in ("cuda", "gpu") for x in ps):
+            return i
+    for i, ps in enumerate(plats):
+        if ps is None:
+            return i
+    raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: lax.platform_dependent without a cuda / gpu branch or a "
+                               "default")
+
+
 def _vec(f, x):
     return T.Vec(f(v) for v in x) if isinstance(x, T.Vec) else f(x)
 
@@ -572,7 +716,8 @@ class _KeyVec(tuple):
 
 
 _RANDOM = {"random_seed": _r_seed, "random_wrap": _r_wrap, "random_unwrap": _r_unwrap, "random_fold_in": _r_fold_in,
-           "random_bits": _r_bits, "random_split": _r_split}
+           "random_bits": _r_bits, "random_split": _r_split, "random_key_data": _r_unwrap,
+           "random_clone": lambda it, e, a: [a[0]]}
 
 
 # ------------------------------------------------------------------------------------------------ the item

@@ -180,6 +180,66 @@ def test_constant_folding_and_lax_integer_semantics():
     assert list(res[2]) == [-3] * 6 and list(res[3]) == [-1] * 6 and np.all(np.asarray(res[4]) == 0.75)
 
 
+def test_vector_structure_primitives():
+    """cumsum / cummax (reverse), rev, pad (interior, negative edge), dot_general (matrix-vector with a constant
+    matrix, and a vector dot), dynamic_update_slice at a traced start, jit (jax >= 0.7's name of pjit),
+    random_clone, iota_2x32_shape and platform_index: the IR evaluator's values bitwise those of numpy float32 in the
+    reference's order (sequential running values; dot sums from zero, acc + x * y, no fused multiply-add)"""
+    from oracle.ir_eval import Evaluator
+    V, E, L = J.Var, J.Eqn, J.Literal
+    x, th, k = V(J.F), V(J.F), V(J.I)
+    x2, xb, x2b, thb, v = V(J.F), V(J.F, (1,)), V(J.F, (1,)), V(J.F, (1,)), V(J.F, (3,))
+    c, r, pd, mv, d, u, cm = V(J.F, (3,)), V(J.F, (3,)), V(J.F, (5,)), V(J.F, (2,)), V(J.F), V(J.F, (5,)), V(J.F, (3,))
+    jin, jout, jv = V(J.F, (3,)), V(J.F, (3,)), V(J.F, (3,))
+    inner = J.ClosedJaxpr(J.Jaxpr([jin], [jout], [J.Eqn("rev", [jin], [jout], dimensions=(0,))]))
+    hi, lo = V(J.U, (4,)), V(J.U, (4,))
+    M = L(np.array([[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]], np.float32), J.F)
+    M.aval = J.Aval((2, 3), J.F)
+    eqns = [E("mul", [x, L(2.0, J.F)], [x2]),
+            E("broadcast_in_dim", [x], [xb], shape=(1,), broadcast_dimensions=()),
+            E("broadcast_in_dim", [x2], [x2b], shape=(1,), broadcast_dimensions=()),
+            E("broadcast_in_dim", [th], [thb], shape=(1,), broadcast_dimensions=()),
+            E("concatenate", [xb, x2b, thb], [v], dimension=0),
+            E("cumsum", [v], [c], axis=0, reverse=False),
+            E("jit", [c], [r], jaxpr=inner, name="flip"),
+            E("pad", [r, L(0.5, J.F)], [pd], padding_config=((1, -1, 1),)),
+            E("dot_general", [M, v], [mv], dimension_numbers=(((1,), (0,)), ((), ())), precision=None,
+              preferred_element_type=np.float32),
+            E("dot_general", [v, v], [d], dimension_numbers=(((0,), (0,)), ((), ())), precision=None,
+              preferred_element_type=np.float32),
+            E("dynamic_update_slice", [pd, mv, k], [u]),
+            E("cummax", [v], [cm], axis=0, reverse=True),
+            E("random_clone", [v], [jv]),
+            E("iota_2x32_shape", [], [hi, lo], shape=(4,))]
+    cj = J.ClosedJaxpr(J.Jaxpr([x, k, th], [c, pd, mv, d, u, cm, lo], eqns))
+    fn, specs = FJ.item_function(cj, [], 2)
+    tr = T.trace_item(fn, specs, 2, {})
+    n = 40
+    xs = np.random.default_rng(4).normal(size=n).astype(np.float32)
+    ks = (np.arange(n) % 7 - 1).astype(np.int32)
+    t = np.float32(0.7)
+    res = [np.asarray(v) for v in Evaluator(tr, 1).run([xs, ks], [t])["results"]]
+    f = np.float32
+    for i in range(n):
+        vv = [xs[i], f(xs[i] * f(2)), t]
+        cc = [vv[0], f(vv[0] + vv[1]), f(f(vv[0] + vv[1]) + vv[2])]
+        rr = cc[::-1]
+        pp = [f(0.5), rr[0], f(0.5), rr[1], f(0.5)]
+        mm = [f(f(f(f(0) + f(1 * vv[0])) + f(2 * vv[1])) + f(3 * vv[2])),
+              f(f(f(f(0) + f(4 * vv[0])) + f(5 * vv[1])) + f(6 * vv[2]))]
+        dd = f(f(f(f(0) + f(vv[0] * vv[0])) + f(vv[1] * vv[1])) + f(vv[2] * vv[2]))
+        s0 = int(np.clip(ks[i], 0, 3))
+        uu = pp[:s0] + mm + pp[s0 + 2:]
+        c2 = vv[2]
+        c1 = max(vv[1], c2)
+        c0 = max(vv[0], c1)
+        want = cc + pp + mm + [dd] + uu + [c0, c1, c2] + [0, 1, 2, 3]
+        got = [res[j][i] for j in range(len(want))]
+        assert np.array_equal(np.float32(got[:-4]).view(np.uint32), np.float32(want[:-4]).view(np.uint32)), i
+        assert got[-4:] == [0, 1, 2, 3]
+    assert FJ._platform_index([("cpu",), ("cuda", "rocm"), None]) == 1 and FJ._platform_index([("cpu",), None]) == 1
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
