@@ -27,7 +27,7 @@ bits / split, threefry2x32), while (the item's one top-level loop), cond (its br
 the taken branch), scan of a static length (unrolled; jax's static fori_loop), pjit and the call wrappers, shape
 operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
 dynamic_update_slice, concatenate, pad, rev, iota, reductions, cumsum / cumprod / cummax / cummin, dot_general with
-a result of at most one dimension), jit (jax >= 0.7's name for pjit), random_clone / random_key_data,
+a result of at most one dimension, sort on one key), jit (jax >= 0.7's name for pjit), random_clone / random_key_data,
 iota_2x32_shape and platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a
 primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
 
@@ -344,6 +344,8 @@ class _Interp:
                  "reduce_or": tl.any, "argmax": tl.argmax, "argmin": tl.argmin}[p]
             return [f(_py(x))]
 
+        if p == "sort":
+            return _sort(a, int(prm.get("num_keys", 1)), tuple(e.invars[0].aval.shape))
         if p == "rev":
             (x,) = a
             return [T.Vec(reversed(list(x))) if isinstance(x, T.Vec) else x]
@@ -640,6 +642,24 @@ def _dynamic_update_slice(x, upd, start):
                 r = tl.where(s == j - i, _py(us[i]), r)
         out.append(r)
     return T.Vec(out)
+
+
+def _sort(ops, num_keys, shape):
+    """lax.sort of vectors on the first operand (jnp.sort; jnp.argsort sorts (x, iota)): stable, ascending in
+    lax.sort's total order -- NaNs last, -0 equal to +0 -- the other operands permuted with it (the reference's
+    stable insertion sort gives the same order, backends/kernel/op_table.py:1006-1044)"""
+    if num_keys != 1:
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a sort on more than one key")
+    if len(shape) > 1:
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a sort of more than one dimension")
+    if shape == () or len(ops[0]) <= 1:
+        return list(ops)
+    if all(_isconst(x) for x in ops):
+        k = np.array(list(ops[0]))
+        order = np.argsort(np.where(k == 0, np.zeros_like(k), k), kind="stable")
+        return [T.Vec(list(x)[i] for i in order) for x in ops]
+    v, rest = tl._sort_network(_py(ops[0]), [_py(x) for x in ops[1:]])
+    return [v] + rest
 
 
 def _platform_index(platforms):

@@ -660,12 +660,13 @@ def searchsorted(a, v, side="left"):
     return cnt
 
 
-def _sorted_pairs(xs):
-    """odd-even transposition sort of a vector with its indices: n passes of adjacent compare-exchanges, a swap
-    when the right element is smaller or the left is NaN (NaNs last, as jnp.sort); equal elements never swap, so
-    the order is stable"""
-    v = list(tuple(xs))
-    idx = list(range(len(v)))
+def _sort_network(keys, payloads=()):
+    """odd-even transposition sort of a vector of keys, each payload vector permuted with it: n passes of adjacent
+    compare-exchanges, a swap when the right key is smaller or the left is NaN (NaNs last, as jnp.sort and lax.sort's
+    total order; -0 and +0 compare equal); equal keys never swap, so the order is stable.  -> (sorted keys, [the
+    payloads in that order])"""
+    v = list(tuple(keys))
+    ps = [list(tuple(q)) for q in payloads]
     n = len(v)
     for p in range(n):
         for j in range(p % 2, n - 1, 2):
@@ -673,8 +674,15 @@ def _sorted_pairs(xs):
             flt = any((isinstance(z, T.Var) and z.dtype == T.F32) or isinstance(z, float) for z in (a, b))
             swap = (b < a) | ((a != a) & (b == b)) if flt else (b < a)
             v[j], v[j + 1] = where(swap, b, a), where(swap, a, b)
-            idx[j], idx[j + 1] = where(swap, idx[j + 1], idx[j]), where(swap, idx[j], idx[j + 1])
-    return T.Vec(v), T.Vec(idx)
+            for q in ps:
+                q[j], q[j + 1] = where(swap, q[j + 1], q[j]), where(swap, q[j], q[j + 1])
+    return T.Vec(v), [T.Vec(q) for q in ps]
+
+
+def _sorted_pairs(xs):
+    """the sorted vector and its stable ascending order's indices"""
+    v, (idx,) = _sort_network(xs, [list(range(len(tuple(xs))))])
+    return v, idx
 
 
 def sort(xs):

@@ -240,6 +240,38 @@ def test_vector_structure_primitives():
     assert FJ._platform_index([("cpu",), ("cuda", "rocm"), None]) == 1 and FJ._platform_index([("cpu",), None]) == 1
 
 
+def test_sort_primitive():
+    """lax.sort of (keys, iota) (jnp.argsort's form) and of keys alone: stable and ascending in lax.sort's total order
+    (NaNs last, -0 equal to +0, each value keeping its bits), bitwise against numpy's stable argsort"""
+    from oracle.ir_eval import Evaluator
+    V, E, L = J.Var, J.Eqn, J.Literal
+    x, y, z = V(J.F), V(J.F), V(J.F)
+    xb, yb, zb, nb = V(J.F, (1,)), V(J.F, (1,)), V(J.F, (1,)), V(J.F, (1,))
+    v, io, sv, perm, sv2 = V(J.F, (5,)), V(J.I, (5,)), V(J.F, (5,)), V(J.I, (5,)), V(J.F, (5,))
+    b = lambda s_, d_: E("broadcast_in_dim", [s_], [d_], shape=(1,), broadcast_dimensions=())
+    eqns = [b(x, xb), b(y, yb), b(z, zb), b(L(-0.0, J.F), nb),
+            E("concatenate", [xb, nb, yb, zb, xb], [v], dimension=0),
+            E("iota", [], [io], dtype=np.int32, shape=(5,), dimension=0, sharding=None),
+            E("sort", [v, io], [sv, perm], dimension=0, is_stable=True, num_keys=1),
+            E("sort", [v], [sv2], dimension=0, is_stable=True, num_keys=1)]
+    cj = J.ClosedJaxpr(J.Jaxpr([x, y, z], [sv, perm, sv2], eqns))
+    fn, specs = FJ.item_function(cj, [], 3)
+    tr = T.trace_item(fn, specs, 3, {})
+    vals = np.float32([0.0, -0.0, 1.5, -2.0, np.nan, -np.nan, np.inf, -np.inf, 1.5])
+    g = np.array(np.meshgrid(vals, vals, vals)).reshape(3, -1)
+    xs, ys, zs = (g[i].astype(np.float32) for i in range(3))
+    res = [np.asarray(r) for r in Evaluator(tr, 1).run([xs, ys, zs], [])["results"]]
+    for i in range(len(xs)):
+        key = np.float32([xs[i], -0.0, ys[i], zs[i], xs[i]])
+        order = np.argsort(np.where(key == 0, np.float32(0), key), kind="stable")
+        got_v = np.float32([res[j][i] for j in range(5)])
+        got_p = [int(res[5 + j][i]) for j in range(5)]
+        got_v2 = np.float32([res[10 + j][i] for j in range(5)])
+        assert got_p == list(order), (key, got_p, order)
+        assert np.array_equal(got_v.view(np.uint32), key[order].view(np.uint32))
+        assert np.array_equal(got_v2.view(np.uint32), key[order].view(np.uint32))
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
