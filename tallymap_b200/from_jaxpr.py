@@ -27,8 +27,9 @@ bits / split, threefry2x32), while (the item's one top-level loop), cond (its br
 the taken branch), scan of a static length (unrolled; jax's static fori_loop), pjit and the call wrappers, shape
 operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
 dynamic_update_slice, concatenate, pad, rev, iota, reductions, cumsum / cumprod / cummax / cummin, dot_general with
-a result of at most one dimension, sort on one key), jit (jax >= 0.7's name for pjit), random_clone / random_key_data,
-iota_2x32_shape and platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a
+a result of at most one dimension, sort on one key, gather as jnp indexing writes it -- a broadcast array of two
+dimensions or above 64 elements is a table read by index --), jit (jax >= 0.7's name for pjit), random_clone /
+random_key_data, iota_2x32_shape and platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a
 primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
 
 `run(p, pi, bc, target, cuda_math, schedule, ndev, min_blocks_per_sm)` is the reference's backend entry
@@ -49,10 +50,16 @@ def _is_key(aval):
     return "key" in str(aval.dtype)
 
 
-def aval_spec(aval):
+def aval_spec(aval, per_item=True):
     """the trace_item input spec of a jaxpr input: "f32" / "i32" / "u32" / "key" for a scalar, (dtype, n) for a
-    small vector"""
+    small vector; a broadcast array of two dimensions, or of one above BC_VECTOR_MAX elements, is a table
+    ("table", dtype, shape), read by index (as tallymap_b200.vmap passes it)"""
     shape = tuple(aval.shape)
+    from .api import BC_VECTOR_MAX
+    dt0 = _DT.get(str(aval.dtype))
+    if not per_item and not _is_key(aval) and dt0 in (T.F32, T.I32) and (
+            len(shape) == 2 or (len(shape) == 1 and (shape[0] > BC_VECTOR_MAX or dt0 == T.I32))):
+        return ("table", dt0, shape)
     if _is_key(aval):
         if shape != ():
             raise T.UnsupportedError("tallymap_b200.from_jaxpr: a per-item key operand must be one key")
@@ -318,6 +325,10 @@ class _Interp:
             s0, s1 = int(prm["start_indices"][0]), int(prm["limit_indices"][0])
             st = int(prm["strides"][0]) if prm.get("strides") else 1
             return [T.Vec(tuple.__getitem__(x, i) for i in range(s0, s1, st))]
+        if p == "gather":
+            return [_gather(e, a[0], a[1], prm)]
+        if p == "dynamic_slice" and isinstance(a[0], T.Table) and len(a[0].shape) == 2:
+            return [_table_slice(a[0], [_py(v) for v in a[1:3]], [int(d) for d in prm["slice_sizes"]])]
         if p == "dynamic_slice":
             x, i = a[0], a[1]
             size = int(prm["slice_sizes"][0])
@@ -370,7 +381,10 @@ class _Interp:
         if p == "platform_index":
             return [np.int32(_platform_index(prm["platforms"]))]
 
-        # elementwise
+        # elementwise (on scalars and vectors: a result with two dimensions above 1 would be a broadcast matrix)
+        if out_aval is not None and sum(int(d) != 1 for d in out_aval.shape) > 1:
+            raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of arrays of shape {tuple(out_aval.shape)} "
+                                       "is not lowered")
         if p == "select_n":
             which, *cases = a
             if _isconst(which) and not isinstance(which, T.Vec):
@@ -472,8 +486,9 @@ class _Interp:
                     raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of {len(x)} elements to a scalar")
                 x = tuple.__getitem__(x, 0)
             return T.Vec([x]) if shape == (1,) else x
-        if len(shape) != 1:
+        if sum(d != 1 for d in shape) > 1:
             raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: arrays of shape {shape} are not lowered")
+        # (a shape with at most one dimension above 1, as (k, 1) gather indices: its row-major elements)
         if isinstance(x, T.Vec):
             if len(x) == n:
                 return x
@@ -662,6 +677,98 @@ def _sort(ops, num_keys, shape):
     return [v] + rest
 
 
+def _mode(mode):
+    """a gather's index mode (GatherScatterMode): 'fill' (out-of-range starts read the fill value), else 'clip'
+    (clip and promise_in_bounds: the start clamped so the slice fits, XLA's gather)"""
+    m = str(mode).upper()
+    if "ONE_HOT" in m:
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a one-hot gather")
+    return "fill" if ("FILL" in m or "DROP" in m) else "clip"
+
+
+def _read(x, idx, shape):
+    """operand x (a Vec, a table or a scalar) at the in-range multi-index idx (static ints or traced int32)"""
+    if isinstance(x, T.Table):
+        return x[tuple(idx)] if len(idx) > 1 else x[idx[0]]
+    if not isinstance(x, T.Vec):
+        return x
+    flat = None
+    for i, n in zip(idx, shape):
+        flat = i if flat is None else flat * n + i
+    if isinstance(flat, (int, np.integer)):
+        return tuple.__getitem__(x, int(flat))
+    return x[flat]
+
+
+def _table_slice(tab, starts, sizes):
+    """lax.dynamic_slice of a 2-D table: one element (sizes (1, 1)) or one whole row (sizes (1, m)), the starts
+    clamped so the slice fits"""
+    (n, m), (s0, s1) = tab.shape, sizes
+    if s0 != 1 or s1 not in (1, m):
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a dynamic_slice of a table other than an element or "
+                                   "a row")
+    i = _clamp_start(starts[0], n - 1)
+    if s1 == m:
+        return T.Vec(tab[i]) if m > 1 else T.Vec([tab[i, 0]])
+    return T.Vec([tab[i, _clamp_start(starts[1], m - 1)]])
+
+
+def _clamp_start(i, hi):
+    if isinstance(i, (int, np.integer)):
+        return int(np.clip(int(i), 0, hi))
+    return tl.clip(i, 0, hi)
+
+
+def _gather(e, x, idx, prm):
+    """lax.gather in the forms jnp indexing writes for 1-D and 2-D operands: each index vector (the last axis of
+    the indices) starts a slice of `slice_sizes`, the collapsed dimensions dropped, the rest kept; the result at
+    most one-dimensional.  Out-of-range starts are clamped so the slice fits (mode clip / promise_in_bounds), or read
+    the fill value (mode fill: NaN for floats, the type's minimum for int32 unless fill_value is given) -- the
+    reference's gather rule, backends/kernel/op_table.py:1085-1180"""
+    dn = prm["dimension_numbers"]
+    oshape = tuple(e.invars[0].aval.shape)
+    ishape = tuple(e.invars[1].aval.shape)
+    sizes = [int(d) for d in prm["slice_sizes"]]
+    if tuple(getattr(dn, "operand_batching_dims", ()) or ()):
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a batched gather")
+    smap = [int(d) for d in dn.start_index_map]
+    collapsed = set(int(d) for d in dn.collapsed_slice_dims)
+    K = ishape[-1] if ishape else 1
+    nb = int(np.prod(ishape[:-1], dtype=np.int64)) if len(ishape) > 1 else 1
+    kept = [d for d in range(len(oshape)) if d not in collapsed]
+    ksize = [sizes[d] for d in kept]
+    if len(ishape) > 2 or (nb > 1 and any(k > 1 for k in ksize)) or sum(k > 1 for k in ksize) > 1:
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a gather whose result has more than one dimension")
+    mode = _mode(prm.get("mode"))
+    iv = list(idx) if isinstance(idx, T.Vec) else [idx]
+    odt = _dtype(e.outvars[0].aval)
+    fill = prm.get("fill_value")
+    if fill is None:
+        fill = float("nan") if odt == T.F32 else -2 ** 31
+    out = []
+    for b in range(nb):
+        starts, ok = [0] * len(oshape), None
+        for q, d in enumerate(smap):
+            s_ = _py(iv[b * K + q])
+            hi = oshape[d] - sizes[d]
+            if mode == "fill" and not isinstance(s_, int):
+                inr = (s_ >= 0) & (s_ <= hi)
+                ok = inr if ok is None else ok & inr
+            elif mode == "fill" and not 0 <= s_ <= hi:
+                ok = False
+            starts[d] = _clamp_start(s_, hi)
+        for off in np.ndindex(*[sizes[d] for d in range(len(oshape))]):
+            pos = [starts[d] + off[d] if off[d] else starts[d] for d in range(len(oshape))]
+            v = _read(x, pos, oshape)
+            if ok is False:
+                v = _NP[odt](fill) if odt in _NP else fill
+            elif ok is not None:
+                v = tl.where(ok, _py(v), fill if odt == T.F32 else int(fill))
+            out.append(v)
+    shape = tuple(e.outvars[0].aval.shape)
+    return out[0] if shape == () or (len(out) == 1 and not shape) else T.Vec(out)
+
+
 def _platform_index(platforms):
     """lax.platform_dependent's branch index for a CUDA device: the branch naming cuda / gpu, else the default
     (the reference's rule, backends/kernel/op_table.py:1650-1659)"""
@@ -747,7 +854,7 @@ def item_function(closed, tallies, n_per_item):
     (a spawn queue token named '__spawn__'); in_specs: trace_item's spec of each leaf."""
     jaxpr = getattr(closed, "jaxpr", closed)
     nT = len(tallies)
-    specs = [aval_spec(v.aval) for v in jaxpr.invars[nT:]]
+    specs = [aval_spec(v.aval, j < n_per_item) for j, v in enumerate(jaxpr.invars[nT:])]
 
     def fn(t, *leaves):
         it = _Interp(t)

@@ -272,6 +272,60 @@ def test_sort_primitive():
         assert np.array_equal(got_v2.view(np.uint32), key[order].view(np.uint32))
 
 
+def test_gather_and_table_slices():
+    """lax.gather as jnp indexing writes it -- a scalar index into a broadcast table (clip and fill modes), a vector
+    of indices into a per-item vector, an element and a row of a 2-D table -- and dynamic_slice of a 2-D table's
+    row: broadcast arrays become tables (as tallymap_b200.vmap passes them); the IR evaluator's values equal numpy's
+    clamped reads, NaN where a fill-mode start is out of range"""
+    from types import SimpleNamespace as NS
+    from oracle.ir_eval import Evaluator
+    V, E, L = J.Var, J.Eqn, J.Literal
+    dn = lambda off, col, smap: NS(offset_dims=off, collapsed_slice_dims=col, start_index_map=smap,
+                                   operand_batching_dims=(), start_indices_batching_dims=())
+    PROM, FILL = "GatherScatterMode.PROMISE_IN_BOUNDS", "GatherScatterMode.FILL_OR_DROP"
+    i, j, vec, tab, tab2 = V(J.I), V(J.I), V(J.F, (4,)), V(J.F, (100,)), V(J.F, (8, 3))
+    ib, ij, i3, g1, g2, g3, g4, g5, ds, row = (V(J.I, (1,)), V(J.I, (2,)), V(J.I, (3, 1)), V(J.F), V(J.F),
+                                              V(J.F, (3,)), V(J.F), V(J.F, (3,)), V(J.F, (1, 3)), V(J.F, (3,)))
+    jb, iv = V(J.I, (1,)), V(J.I, (3,))
+    b = lambda s_, d_, shape=(1,): E("broadcast_in_dim", [s_], [d_], shape=shape, broadcast_dimensions=())
+    eqns = [b(i, ib), b(j, jb),
+            E("concatenate", [ib, jb], [ij], dimension=0),
+            E("concatenate", [ib, jb, ib], [iv], dimension=0),
+            E("reshape", [iv], [i3], new_sizes=(3, 1), dimensions=None),
+            E("gather", [tab, ib], [g1], dimension_numbers=dn((), (0,), (0,)), slice_sizes=(1,), mode=PROM,
+              fill_value=None, indices_are_sorted=False, unique_indices=False),
+            E("gather", [tab, ib], [g2], dimension_numbers=dn((), (0,), (0,)), slice_sizes=(1,), mode=FILL,
+              fill_value=None, indices_are_sorted=False, unique_indices=False),
+            E("gather", [vec, i3], [g3], dimension_numbers=dn((), (0,), (0,)), slice_sizes=(1,), mode=PROM,
+              fill_value=None, indices_are_sorted=False, unique_indices=False),
+            E("gather", [tab2, ij], [g4], dimension_numbers=dn((), (0, 1), (0, 1)), slice_sizes=(1, 1), mode=PROM,
+              fill_value=None, indices_are_sorted=False, unique_indices=False),
+            E("gather", [tab2, ib], [g5], dimension_numbers=dn((0,), (0,), (0,)), slice_sizes=(1, 3), mode=PROM,
+              fill_value=None, indices_are_sorted=False, unique_indices=False),
+            E("dynamic_slice", [tab2, j, L(0, J.I)], [ds], slice_sizes=(1, 3)),
+            E("reshape", [ds], [row], new_sizes=(3,), dimensions=None)]
+    cj = J.ClosedJaxpr(J.Jaxpr([i, j, vec, tab, tab2], [g1, g2, g3, g4, g5, row], eqns))
+    fn, specs = FJ.item_function(cj, [], 3)
+    assert specs[3:] == [("table", "f32", (100,)), ("table", "f32", (8, 3))]
+    tr = T.trace_item(fn, specs, 3, {})
+    rng = np.random.default_rng(8)
+    n = 60
+    ii = rng.integers(-5, 110, n).astype(np.int32)
+    jj = rng.integers(-2, 10, n).astype(np.int32)
+    vv = rng.normal(size=(n, 4)).astype(np.float32)
+    t1 = rng.normal(size=100).astype(np.float32)
+    t2 = rng.normal(size=(8, 3)).astype(np.float32)
+    res = [np.asarray(r) for r in Evaluator(tr, 1).run([ii, jj, vv], [t1, t2])["results"]]
+    for q in range(n):
+        c1 = int(np.clip(ii[q], 0, 99))
+        want = [t1[c1], t1[ii[q]] if 0 <= ii[q] < 100 else np.nan]
+        want += [vv[q, int(np.clip(z, 0, 3))] for z in (ii[q], jj[q], ii[q])]
+        want += [t2[int(np.clip(ii[q], 0, 7)), int(np.clip(jj[q], 0, 2))]]
+        want += list(t2[int(np.clip(ii[q], 0, 7))]) + list(t2[int(np.clip(jj[q], 0, 7))])
+        got = [res[z][q] for z in range(len(want))]
+        assert np.array_equal(np.float32(got), np.float32(want), equal_nan=True), q
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
