@@ -221,6 +221,20 @@ class Evaluator:
     def _run_eqns(self, eqns, env, out):
         for e in eqns:
             a = [self._val(x, env) for x in e.ins]
+            if e.prim == "while":                  # (an inner loop: its condition and body until the condition fails)
+                prm = e.params
+                vals = a
+                while True:
+                    for cv, v in zip(prm["carry"], vals):
+                        env[cv.id] = v
+                    self._run_eqns(prm["cond"], env, out)
+                    if not bool(self._val(prm["cond_out"], env)):
+                        break
+                    self._run_eqns(prm["body"], env, out)
+                    vals = [self._val(x, env) for x in prm["body_out"]]
+                for o, v in zip(e.outs, vals):
+                    env[o.id] = v
+                continue
             if e.prim == "claim":                  # (a Records slot claim: the launch's counter, in item order)
                 nm, c = e.params["tally"], self._claims.get(e.params["tally"], 0)
                 if a[0]:

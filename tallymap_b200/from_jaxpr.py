@@ -502,9 +502,6 @@ class _Interp:
         prm = e.params
         cn, bn = int(prm["cond_nconsts"]), int(prm["body_nconsts"])
         cconst, bconst, init = a[:cn], a[cn:cn + bn], a[cn + bn:]
-        if self.depth > 0:
-            raise T.UnsupportedError("tallymap_b200.from_jaxpr: a while loop inside the item's loop (nested loops "
-                                     "are not lowered)")
         self.depth += 1
         try:
             flat = [(_py(x) if not isinstance(x, T.Vec) else _py(x)) for x in init]

@@ -298,6 +298,16 @@ def _predicate(tr, n0, taken):
         tr.eqns[n0:n0] = new
     out = tr.eqns[:n0]
     for e in tr.eqns[n0:]:
+        if e.prim == "while" and not (isinstance(taken, T.Lit) and taken.value):
+            # (an inner loop in a branch iterates only where the branch is taken: its condition ANDed with the
+            # predicate, so a loop that would not end on the other branch's values never starts, and the effects
+            # in its body need no predicate of their own)
+            p = dict(e.params)
+            c = tr.new(T.BOOL)
+            p["cond"] = list(p["cond"]) + [T.Eqn("and", [p["cond_out"], taken], [c], {})]
+            p["cond_out"] = c
+            out.append(T.Eqn("while", e.ins, e.outs, p))
+            continue
         if e.prim not in _EFFECTS:
             out.append(e)
             continue
@@ -322,13 +332,21 @@ def _predicate(tr, n0, taken):
 
 
 def _branches(funs, operands, picks):
-    """trace each branch on the same operands, its effects (t.add, t.append, t.spawn) predicated on picks[j]"""
+    """trace each branch on the same operands, its effects (t.add, t.append, t.spawn) predicated on picks[j]; a
+    while loop in a branch is an inner loop (never the item's stepping loop), run only where its branch is taken"""
     tr = T._cur()
+    st = getattr(tr, "loop_state", None)
     res = []
     for f, taken in zip(funs, picks):
         n0 = len(tr.eqns)
-        res.append(f(*operands))
-        if builtins.any(e.prim in _EFFECTS for e in tr.eqns[n0:]):
+        if st is not None:
+            st["branch"] = st.get("branch", 0) + 1
+        try:
+            res.append(f(*operands))
+        finally:
+            if st is not None:
+                st["branch"] -= 1
+        if builtins.any(e.prim in _EFFECTS or e.prim == "while" for e in tr.eqns[n0:]):
             _predicate(tr, n0, taken)
     return res
 
@@ -359,11 +377,14 @@ def switch(index, branches, *operands):
 
 
 def fori_loop(lower, upper, body_fun, init_val):
-    """lax.fori_loop with Python int bounds: the body applied upper - lower times, unrolled (an inner loop of a
-    static trip count; the item's one top-level loop stays lax.while_loop)"""
+    """lax.fori_loop: with Python int bounds the body applied upper - lower times, unrolled (a static trip count);
+    with a traced bound, jax's while form -- (i, val) carried while i < upper, an inner loop"""
     if not (isinstance(lower, int) and isinstance(upper, int)):
-        raise T.UnsupportedError("tallymap_b200.lang.fori_loop: Python int bounds only (a traced trip count is a "
-                                 "while_loop)")
+        lo = T._lit(lower)
+        hi = T._lit(upper)
+        if lo.dtype != T.I32 or hi.dtype != T.I32:
+            raise T.TraceError("tallymap_b200.lang.fori_loop: int32 bounds")
+        return while_loop(lambda c: c[0] < upper, lambda c: (c[0] + 1, body_fun(c[0], c[1])), (lower, init_val))[1]
     if upper - lower > 4096:
         raise T.UnsupportedError("tallymap_b200.lang.fori_loop: at most 4096 unrolled iterations")
     v = init_val

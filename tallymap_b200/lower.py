@@ -228,10 +228,19 @@ def _ids(xs):
 
 
 def _uses(eqns):
+    """the variables `eqns` read, an inner while loop's reads of values defined before it included"""
     u = set()
     for e in eqns:
         u |= _ids(e.ins)
+        if e.prim == "while":
+            p = e.params
+            inner = _uses(p["cond"]) | _uses(p["body"]) | _ids(p["body_out"]) | _ids([p["cond_out"]])
+            u |= inner - _defs_deep(p["cond"] + p["body"]) - _ids(p["carry"])
     return u
+
+
+def _defs_deep(eqns):
+    return {o.id for e in T._walk(eqns) for o in e.outs}
 
 
 def _defs(eqns):
@@ -273,7 +282,7 @@ class Item:
         if self.spawns and tr.records:
             raise NotImplementedError("tallymap_b200: Records outputs of a spawning item are not lowered")
         # Records slot claims of the jaxpr front end: one launch counter per claimed tally (by its output position)
-        self.claims = any(e.prim == "claim" for e in tr.pre + tr.body + tr.post)
+        self.claims = any(e.prim == "claim" for e in T._walk(tr.pre + tr.body + tr.post))
         if self.claims and self.spawns:
             raise NotImplementedError("tallymap_b200: Records slot claims in a spawning item are not lowered")
         # step counters: carries that start at 0 and gain 1 per step equal the step index (not stored by the replay)
@@ -375,6 +384,25 @@ def _emit_code(eqns, names, emitter, indent="    ", skip_emits=False, appender=N
         if e.prim == "append":
             if appender is not None:
                 out.append(indent + appender(e.params["records"], a[0], a[1:]))
+            continue
+        if e.prim == "while":
+            # an inner loop (the reference's while rule, backends/kernel/op_table.py:1414-1450): its carry in
+            # mutable locals, the condition and body re-evaluated each iteration, the next carry through temporaries
+            p = e.params
+            for o, x in zip(e.outs, e.ins):
+                out.append(f"{indent}{CTYPE[o.dtype]} v{o.id} = {_ref(x, names)};")
+                names[o.id] = f"v{o.id}"
+            for cv, o in zip(p["carry"], e.outs):
+                names[cv.id] = f"v{o.id}"
+            out.append(f"{indent}while (true) {{")
+            sub = dict(skip_emits=skip_emits, appender=appender, spawner=spawner, claimer=claimer)
+            out += _emit_code(p["cond"], names, emitter, indent + "  ", **sub)
+            out.append(f"{indent}  if (!({_ref(p['cond_out'], names)})) break;")
+            out += _emit_code(p["body"], names, emitter, indent + "  ", **sub)
+            nxt = [f"const {CTYPE[o.dtype]} n{o.id} = {_ref(b, names)};" for o, b in zip(e.outs, p["body_out"])]
+            out += [indent + "  " + x for x in nxt]
+            out += [f"{indent}  v{o.id} = n{o.id};" for o in e.outs]
+            out.append(f"{indent}}}")
             continue
         if e.prim == "claim":
             if claimer is None:
@@ -803,7 +831,7 @@ def _draw_split(it):
     fixed = set(it.saved) | set(it.bc_ids) | {tr.carry[j].id for j in it.counter}
     draws, rest, dset = [], [], set()
     for e in tr.body:
-        ok = e.prim not in ("emit", "spawn", "append", "claim") and \
+        ok = e.prim not in ("emit", "spawn", "append", "claim", "while") and \
             all(not isinstance(x, T.Var) or x.id in fixed or x.id in dset for x in e.ins)
         if ok:
             draws.append(e)
@@ -941,7 +969,7 @@ def _active(it, wrt, extra=()):
             if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop", "gather") \
                     or not e.outs:
                 continue
-            if any(isinstance(x, T.Var) and x.id in act for x in e.ins):
+            if e.prim == "while" and _uses([e]) & act or any(isinstance(x, T.Var) and x.id in act for x in e.ins):
                 for o in e.outs:
                     if o.dtype == T.F32:
                         act.add(o.id)
@@ -987,6 +1015,11 @@ class _Rev:
 
     def run(self, eqns, names, ct_tally):
         for e in reversed(eqns):
+            if e.prim == "while":
+                if _uses([e]) & self.active:
+                    raise LowerError("tallymap_b200.lower: reverse mode through an inner while loop that reads a "
+                                     "differentiated value is not lowered (its iterations would need a tape)")
+                continue
             if e.prim == "spawn":
                 if self.spawn_t is not None:
                     self.spawn_t(self, e, names)
@@ -1883,6 +1916,14 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
     out = []
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
+        if e.prim == "while":
+            if _uses([e]) & (set(act) | set(tnames)):
+                raise LowerError("tallymap_b200.lower: forward mode through an inner while loop that reads a "
+                                 "differentiated value is not lowered")
+            # (no tangent inside: the loop as the forward runs it; its appends carry zero field tangents)
+            app = None if appender is None else (lambda rn, w, vals: appender(rn, w, vals, [None] * len(vals)))
+            out += _emit_code([e], names, emitter, indent, appender=app)
+            continue
         if e.prim == "spawn":
             if spawner is not None:
                 tl = [tnames.get(x.id) if isinstance(x, T.Var) else None for x in e.ins[1:]]

@@ -7,9 +7,11 @@ jaxpr-like IR:
 
     Eqn(prim, ins, outs, params)   ins: Var or Lit; outs: Var
 
-with dtypes f32, i32, u32 and bool.  The item must have exactly ONE top-level while loop (the reference's step
-schedule needs the same: backends/kernel/kernel.py:225-295 splits an item into pre / cond / body / post), so a traced
-item is four equation lists: `pre` (before the loop), `cond` and `body` (on the loop carry), `post` (after it).
+with dtypes f32, i32, u32 and bool.  The item's first top-level while loop is its stepping loop (the reference's
+step schedule splits an item the same way: backends/kernel/kernel.py:225-295 into pre / cond / body / post), so a
+traced item is four equation lists: `pre` (before the loop), `cond` and `body` (on the loop carry), `post` (after
+it).  Any other while loop -- inside the stepping loop, inside a cond branch, after it -- is ONE equation "while"
+holding its own condition and body lists (an inner loop; _nested_while).
 
 Emits (`t.add(name, index, value)`) are equations of prim "emit"; a tuple index is flattened row-major with any
 out-of-range coordinate giving -1 (tallymap/_tally.py:248-282), which the lowering drops and counts in stats[4].
@@ -589,15 +591,73 @@ class _Loop:
     pass
 
 
+def _walk(eqns):
+    """every equation of `eqns`, those inside nested while loops included"""
+    for e in eqns:
+        yield e
+        if e.prim == "while":
+            yield from _walk(e.params["cond"])
+            yield from _walk(e.params["body"])
+
+
+def _nested_while(cond_fun, body_fun, init):
+    """a while loop other than the item's stepping loop -- inside its body or condition, or after it -- as ONE
+    equation "while" whose params hold its own condition and body (the reference's emitter writes it as a C while
+    loop, op_table.py:1414-1450): ins = the initial carry (the tally handle passes through in its position), outs =
+    the final carry; the condition and body may read any value defined before the loop.  A spawn inside it is not
+    lowered (a step pushes at most two children)."""
+    tr = _cur()
+    flat_in, rebuild = _flatten(init)
+    cond_tr, body_tr = Trace(tr.ids), Trace(tr.ids)
+    carry = []
+    for x in flat_in:
+        carry.append(x if isinstance(x, TallyToken) else body_tr.new(_lit(x).dtype))
+    _CTX.append(cond_tr)
+    try:
+        c = cond_fun(rebuild(carry))
+    finally:
+        _CTX.pop()
+    if not isinstance(c, Var) or c.dtype != BOOL:
+        raise TraceError("tallymap_b200.lang: a while loop's condition must be a traced bool")
+    if any(e.prim in ("emit", "append", "spawn", "claim") for e in _walk(cond_tr.eqns)):
+        raise TraceError("tallymap_b200.lang: a while loop's condition may not write the tally")
+    _CTX.append(body_tr)
+    try:
+        out = body_fun(rebuild(carry))
+    finally:
+        _CTX.pop()
+    if any(e.prim == "spawn" for e in _walk(body_tr.eqns)):
+        raise UnsupportedError("tallymap_b200.lang: t.spawn inside an inner while loop is not lowered (spawn in "
+                               "the item's loop body or after it)")
+    flat_out, _ = _flatten(out)
+    if len(flat_out) != len(flat_in):
+        raise TraceError("tallymap_b200.lang: the loop body must return a carry of the same structure")
+    cvars, body_out = [], []
+    for a, b, cv in zip(flat_in, flat_out, carry):
+        if isinstance(a, TallyToken) != isinstance(b, TallyToken):
+            raise TallyError("tallymap_b200.lang: the tally handle must stay in its carry position")
+        if isinstance(a, TallyToken):
+            continue
+        v = _lit(b, cv)
+        if v.dtype != cv.dtype:
+            raise TraceError(f"tallymap_b200.lang: a loop carry of {cv.dtype} became {v.dtype} in the body")
+        cvars.append(cv)
+        body_out.append(v)
+    outs = [tr.new(v.dtype) for v in cvars]
+    tr.eqns.append(Eqn("while", [_lit(x) for x in flat_in if not isinstance(x, TallyToken)], outs,
+                       dict(carry=cvars, cond=cond_tr.eqns, cond_out=c, body=body_tr.eqns, body_out=body_out)))
+    it = iter(outs)
+    return rebuild([x if isinstance(x, TallyToken) else next(it) for x in carry])
+
+
 def while_loop(cond_fun, body_fun, init):
-    """the item's top-level loop (lax.while_loop); the carry is a tuple of scalars, keys and the tally handle"""
+    """lax.while_loop; the carry is a tuple of scalars, keys and the tally handle.  The item's first loop at its
+    top level is its stepping loop (the runtime refills threads at its step granularity); any other loop -- inside
+    it, or after it -- is an inner loop (_nested_while)"""
     tr = _cur()
     st = getattr(tr, "loop_state", None)
-    if st is None or st.get("depth", 0) != 0:
-        raise UnsupportedError("tallymap_b200.lang: only ONE top-level while_loop per item "
-                               "(nested loops are not lowered)")
-    if st.get("done"):
-        raise UnsupportedError("tallymap_b200.lang: only one top-level while_loop per item")
+    if st is None or st.get("depth", 0) != 0 or st.get("done") or st.get("branch"):
+        return _nested_while(cond_fun, body_fun, init)
     flat_in, rebuild = _flatten(init)
     carry = []
     body_tr = Trace(tr.ids)

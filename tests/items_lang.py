@@ -527,3 +527,43 @@ def quickstart_hits(t, x, key, theta):
         return k + 1, x * (0.5 + 0.5 * u), t
     k, x, t = tl.while_loop(lambda c: c[1] > 0.05, body, (0, x, t))
     return t, k
+
+
+def rejection(t, x, key, a):
+    """inner while loops (the reference's C while, backends/kernel/op_table.py:1414-1450): each step of the walk
+    draws (u, v) until u^2 + v^2 < 1 (at most 64 tries, a try counted into the int tally inside the inner loop,
+    reading the step's key from outside it) and moves by 0.05 u; a step that starts above a half runs three more
+    inner iterations in a cond branch; after the stepping loop, a second loop halves |x| while above 0.01 and a
+    fori_loop with a traced bound sums 0..k%5-1"""
+    def body(c):
+        k, x, t = c
+        kk = tl.random.fold_in(key, k)
+
+        def draw(d):
+            j, u, v, t = d
+            kj = tl.random.fold_in(kk, j)
+            u = 2.0 * tl.random.uniform(tl.random.fold_in(kj, 0)) - 1.0
+            v = 2.0 * tl.random.uniform(tl.random.fold_in(kj, 1)) - 1.0
+            return j + 1, u, v, t.add("tries", 0, 1)
+        j, u, v, t = tl.while_loop(lambda d: (d[0] < 64) & (d[1] * d[1] + d[2] * d[2] >= 1.0), draw,
+                                   (0, 1.0, 1.0, t))
+        three = lambda tt: tl.while_loop(lambda d: d[0] < 3, lambda d: (d[0] + 1, d[1].add("tries", 1, 1)), (0, tt))[1]
+        t = tl.cond(x > 0.5, three, lambda tt: tt, t)
+        x = x + 0.05 * u
+        t = t.add("h", (x * 8).astype(tl.int32), a * x)
+        return k + 1, x, t
+    k, x, t = tl.while_loop(lambda c: (c[0] < 200) & (c[1] > 0.0) & (c[1] < 1.0), body, (0, x, t))
+    n, y = tl.while_loop(lambda c: (c[0] < 32) & (c[1] > 0.01), lambda c: (c[0] + 1, c[1] * 0.5), (0, tl.abs(x)))
+    t = t.add("h", 8, a * y)
+    s = tl.fori_loop(0, k % 5, lambda i, c: c + i, 0)
+    return t, k, n, s
+
+
+def rejection_active(t, x, key, a):
+    """an inner loop that reads the differentiated operand a: lowered forward, refused by reverse mode"""
+    def body(c):
+        k, x, t = c
+        j, y = tl.while_loop(lambda d: (d[0] < 4) & (d[1] < 1.0), lambda d: (d[0] + 1, d[1] + a), (0, x))
+        return k + 1, x + 0.1, t.add("h", 0, y)
+    k, x, t = tl.while_loop(lambda c: c[0] < 5, body, (0, x, t))
+    return t, k

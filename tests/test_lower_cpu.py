@@ -48,12 +48,12 @@ def test_mixer_compiles_with_all_primitives():
 
 
 def test_trace_errors():
-    def two_loops(t, x, key, d):
+    def two_loops(t, x, key, d):          # (the second loop, after the stepping loop, is an inner loop)
         x = tl.while_loop(lambda c: c > 0.0, lambda c: c - 1.0, x)
         x = tl.while_loop(lambda c: c > 0.0, lambda c: c - 1.0, x)
         return t, x
-    with pytest.raises(T.TraceError, match="one top-level"):
-        T.trace_item(two_loops, ["f32", "key", "f32"], 2, {})
+    tr2 = T.trace_item(two_loops, ["f32", "key", "f32"], 2, {})
+    assert [e.prim for e in tr2.post] == ["while"]
 
     def no_loop(t, x, key, d):        # (a loop-free item: a loop of zero steps, its code after it)
         return t, x
@@ -426,10 +426,10 @@ def test_error_types():
     kernel backend does not lower an UnsupportedError (a NotImplementedError, _api.py:198); both TraceErrors here"""
     def reads(t, x):
         return t, x + t
-    def nested(t, x):
+    def nested(t, x):                     # (a spawn inside an inner loop: a step pushes at most two children)
         def body(c):
             i, t = c
-            j, t = tl.while_loop(lambda d: d[0] < 2, lambda d: (d[0] + 1, d[1]), (0, t))
+            j, t = tl.while_loop(lambda d: d[0] < 2, lambda d: (d[0] + 1, d[1].spawn((x,))), (0, t))
             return i + j, t
         i, t = tl.while_loop(lambda c: c[0] < 4, body, (0, t))
         return t, i
@@ -441,7 +441,7 @@ def test_error_types():
     with pytest.raises(tm.TallyError):
         T.trace_item(drops, ["f32"], 1, specs)
     with pytest.raises(tm.UnsupportedError) as e:
-        T.trace_item(nested, ["f32"], 1, specs)
+        T.trace_item(nested, ["f32"], 1, specs, spawn=True)
     assert isinstance(e.value, NotImplementedError) and isinstance(e.value, T.TraceError)
     assert issubclass(lower.LowerError, tm.UnsupportedError)
 
@@ -1003,3 +1003,71 @@ def test_cond_branches_write_the_tally():
     ra, rb = (Evaluator(T.trace_item(fn, specs, 3, outs, spawn=True), 10).run([g, wv, k2], [np.float32(1.1)])
               for fn in (spawn_decay_cond, spawn_decay))
     assert np.array_equal(ra["sums"]["Q"], rb["sums"]["Q"]) and ra["stats"][0] == rb["stats"][0] == 100
+
+
+def _host_rejection(x0, key, a):
+    """the rejection item (items_lang.rejection) restated with the host PRNG, one item: (h bins, tries, k, n, s)"""
+    f = np.float32
+    h, tries = np.zeros(9), [0, 0]
+    k, x = 0, f(x0)
+    while k < 200 and 0.0 < x < 1.0:
+        kk = prng.fold_in(key, k)
+        j, u, v = 0, f(1.0), f(1.0)
+        while j < 64 and f(f(u * u) + f(v * v)) >= 1.0:
+            kj = prng.fold_in(kk, j)
+            u = f(f(2.0) * prng.uniform(prng.fold_in(kj, 0), 1)[0] - f(1.0))
+            v = f(f(2.0) * prng.uniform(prng.fold_in(kj, 1), 1)[0] - f(1.0))
+            j += 1
+            tries[0] += 1
+        if x > 0.5:
+            tries[1] += 3
+        x = f(x + f(f(0.05) * u))
+        b = int(f(x * f(8.0)))
+        if 0 <= b < 9:
+            h[b] += float(f(a * x))
+        k += 1
+    y, n = f(abs(x)), 0
+    while n < 32 and y > 0.01:
+        n, y = n + 1, f(y * f(0.5))
+    h[8] += float(f(a * y))
+    return h, tries, k, n, sum(range(k % 5))
+
+
+def test_inner_while_loops():
+    """inner while loops -- inside the stepping loop's body (reading the step's key from outside, writing the tally
+    inside), inside a cond branch (iterating only where the branch is taken), after the stepping loop, and a
+    fori_loop with a traced bound -- trace to nested "while" equations that the IR evaluator runs as the host
+    restatement does, bitwise; the forward, reverse, one-pass and forward-mode programs compile when the inner loops
+    read no differentiated value, and reverse / forward mode refuse one that does"""
+    from oracle.ir_eval import Evaluator
+    from items_lang import rejection, rejection_active
+    specs = {"h": ((9,), "f32"), "tries": ((2,), "i32")}
+    tr = T.trace_item(rejection, ["f32", "key", "f32"], 2, specs)
+    assert sum(e.prim == "while" for e in tr.body) == 2 and sum(e.prim == "while" for e in tr.post) == 2
+    n = 24
+    x0 = np.random.default_rng(6).uniform(0.2, 0.8, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(17), n)
+    a = np.float32(1.25)
+    r = Evaluator(tr, 1000).run([x0, keys], [a])
+    h, tries = np.zeros(9), np.zeros(2, np.int64)
+    for i in range(n):
+        hi, ti, k, nn, s_ = _host_rejection(x0[i], keys[i], a)
+        h += hi
+        tries += ti
+        assert (r["results"][0][i], r["results"][1][i], r["results"][2][i]) == (k, nn, s_), i
+    assert np.array_equal(r["sums"]["tries"], tries) and tries[0] > 0 and tries[1] > 0
+    assert np.abs(r["sums"]["h"] - h).max() <= 1e-9 * np.abs(h).max()
+    f = tm.vmap(rejection, outputs={"h": tm.Sum((9,)), "tries": tm.Sum((2,), tm.api.torch.int32)},
+                in_axes=(0, 0, None), max_steps=1000)
+    L = f.lowered((x0, keys, a))
+    src = L.fwd_source
+    assert src.count("while (true)") >= 4
+    assert L.grad_program((0,)).kernel > 0 and L.jvp_program((0,), 1).kernel > 0
+    assert L.vg_program((0,)).kernel > 0
+    g = tm.vmap(rejection_active, outputs={"h": tm.Sum((1,))}, in_axes=(0, 0, None), max_steps=10)
+    La = g.lowered((x0, keys, a))
+    assert La.fwd.kernel > 0
+    with pytest.raises(tm.UnsupportedError, match="inner while loop"):
+        La.grad_program((0,))
+    with pytest.raises(tm.UnsupportedError, match="inner while loop"):
+        La.jvp_program((0,), 1)

@@ -993,3 +993,37 @@ def test_spawn_inside_a_cond_branch(cuda):
         assert f.last_tree["children"] == 2 * 3000 and int(f.last_tree["mismatch"]) == 0
         res.append((np_out(r)["Q"], gw.cpu().numpy(), float(ga)))
     assert near(res[0][0], res[1][0]) and near(res[0][1], res[1][1], 1e-6) and near(res[0][2], res[1][2], 1e-6)
+
+
+def test_inner_while_loops(cuda):
+    """inner while loops (rejection sampling inside the step reading the step's key, three iterations in a cond
+    branch, a halving loop and a traced-bound fori_loop after the stepping loop): trip counts, inner-loop counts and
+    the int tally bitwise the IR evaluator's (run first, so every inner loop is known to end), the float tally within
+    the float tolerance; the replay gradient, the one-pass value-and-grad and forward mode w.r.t. a (the tally is
+    linear in a: its derivative is h / a) within 1e-5"""
+    from items_lang import rejection
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as Tr
+    n = 300
+    x0 = np.random.default_rng(6).uniform(0.2, 0.8, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(17), n)
+    a = np.float32(1.25)
+    specs = {"h": ((9,), "f32"), "tries": ((2,), "i32")}
+    ref = Evaluator(Tr.trace_item(rejection, ["f32", "key", "f32"], 2, specs), 1000).run([x0, keys], [a])
+    f = tm.vmap(rejection, outputs={"h": tm.Sum((9,)), "tries": tm.Sum((2,), torch.int32)}, in_axes=(0, 0, None),
+                max_steps=1000)
+    r = f(x0, keys, a)
+    torch.cuda.synchronize()
+    per = r.per_item if isinstance(r.per_item, (tuple, list)) else (r.per_item,)
+    for j in range(3):
+        assert np.array_equal(per[j].cpu().numpy(), ref["results"][j]), j
+    assert np.array_equal(r.outputs["tries"].cpu().numpy(), ref["sums"]["tries"])
+    assert near(r.outputs["h"].cpu().numpy(), ref["sums"]["h"])
+    ct = torch.linspace(-1.0, 1.0, 9)
+    want = float(np.dot(ct.numpy().astype(np.float64), ref["sums"]["h"] / float(a)))
+    g = f.grad(x0, keys, a, wrt=2, cotangents={"h": ct})
+    _, gv = f.value_and_grad(x0, keys, a, wrt=2, cotangents={"h": ct})
+    _, d = f.jvp(x0, keys, a, wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    assert abs(float(g) - want) <= 1e-5 * abs(want) and abs(float(gv) - want) <= 1e-5 * abs(want)
+    assert near(d["h"].cpu().numpy(), ref["sums"]["h"] / float(a))
