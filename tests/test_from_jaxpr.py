@@ -326,6 +326,49 @@ def test_gather_and_table_slices():
         assert np.array_equal(np.float32(got), np.float32(want), equal_nan=True), q
 
 
+def test_inner_while_in_a_jaxpr():
+    """a while equation inside the item's loop body (jax writes an inner lax.while_loop as a nested while): an inner
+    loop of the trace, as the same item written with lang, bitwise"""
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import lang as tl
+    V, E, L = J.Var, J.Eqn, J.Literal
+    x = V(J.F)
+    # the stepping loop: (k, x) while k < 5; its body runs an inner loop (j, y) = while j < k: (j + 1, y * 0.5 + x)
+    bk, bx, ij, cq, ij2, iy2, t0, jo, yo, bk2, bx2 = (V(J.I), V(J.F), V(J.I), V(J.B), V(J.I), V(J.F), V(J.F), V(J.I),
+                                                      V(J.F), V(J.I), V(J.F))
+    ck, cx, cc, ik = V(J.I), V(J.F), V(J.B), V(J.I)
+    icond = J.ClosedJaxpr(J.Jaxpr([ik, ij, V(J.F)], [cq], [E("lt", [ij, ik], [cq])]))
+    ibx = V(J.F)
+    ibody = J.ClosedJaxpr(J.Jaxpr([ibx, ij2, iy2], [jo, yo], [E("add", [ij2, L(1, J.I)], [jo]),
+                                                             E("mul", [iy2, L(0.5, J.F)], [t0]),
+                                                             E("add", [t0, ibx], [yo])]))
+    jf, yf = V(J.I), V(J.F)
+    body = J.ClosedJaxpr(J.Jaxpr([bk, bx], [bk2, bx2], [
+        E("while", [bk, bx, L(0, J.I), bx], [jf, yf], cond_jaxpr=icond, body_jaxpr=ibody, cond_nconsts=1,
+          body_nconsts=1),
+        E("add", [bk, L(1, J.I)], [bk2]),
+        E("mul", [yf, L(0.75, J.F)], [bx2])]))
+    cond = J.ClosedJaxpr(J.Jaxpr([ck, cx], [cc], [E("lt", [ck, L(5, J.I)], [cc])]))
+    ko, xo = V(J.I), V(J.F)
+    cj = J.ClosedJaxpr(J.Jaxpr([x], [ko, xo], [E("while", [L(0, J.I), x], [ko, xo], cond_jaxpr=cond, body_jaxpr=body,
+                                                    cond_nconsts=0, body_nconsts=0)]))
+    fn, specs = FJ.item_function(cj, [], 1)
+    tr = T.trace_item(fn, specs, 1, {})
+    assert [e.prim for e in tr.body].count("while") == 1
+
+    def item(t, x):
+        def body(c):
+            k, x = c
+            _, y = tl.while_loop(lambda d: d[0] < k, lambda d: (d[0] + 1, d[1] * 0.5 + x), (0, x))
+            return k + 1, y * 0.75
+        k, x = tl.while_loop(lambda c: c[0] < 5, body, (0, x))
+        return t, k, x
+    xs = np.random.default_rng(2).normal(size=32).astype(np.float32)
+    r = Evaluator(tr, 10).run([xs], [])
+    rq = Evaluator(T.trace_item(item, ["f32"], 1, {}), 10).run([xs], [])
+    assert np.array_equal(np.asarray(r["results"][1]).view(np.uint32), np.asarray(rq["results"][1]).view(np.uint32))
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
