@@ -958,6 +958,39 @@ def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
 
 
 # ------------------------------------------------------------------------------------------------ reverse program
+def _prop(eqns, act):
+    """add to `act` the float results that depend on a member of it (an inner loop's: by its carries' fixpoint)"""
+    for e in eqns:
+        if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop", "gather") \
+                or not e.outs:
+            continue
+        if e.prim == "while":
+            if _uses([e]) & act:
+                _, cact = _inner_active(e, act)
+                act.update(o.id for o, a_ in zip(e.outs, cact) if a_)
+            continue
+        if any(isinstance(x, T.Var) and x.id in act for x in e.ins):
+            for o in e.outs:
+                if o.dtype == T.F32:
+                    act.add(o.id)
+
+
+def _inner_active(e, act):
+    """an inner loop's activity: (the active set inside it -- `act` plus its active carries and the body values
+    that depend on them or on active values outside --, per carry whether it is an active float) by a fixpoint over
+    its body, as _active does for the stepping loop"""
+    p = e.params
+    cact = [isinstance(x, T.Var) and x.id in act and cv.dtype == T.F32 for x, cv in zip(e.ins, p["carry"])]
+    while True:
+        inner = set(act) | {cv.id for cv, a_ in zip(p["carry"], cact) if a_}
+        _prop(p["body"], inner)
+        new = [cact[j] or (isinstance(b, T.Var) and b.id in inner and p["carry"][j].dtype == T.F32)
+               for j, b in enumerate(p["body_out"])]
+        if new == cact:
+            return inner, cact
+        cact = new
+
+
 def _active(it, wrt, extra=()):
     """float variables that depend on the differentiated broadcast operands (tallymap/_reverse.py:208 `_active`);
     extra: more seeds (a spawning item's float per-item inputs: a child's may carry tangents)"""
@@ -965,14 +998,7 @@ def _active(it, wrt, extra=()):
     act = {it.bc[k].id for k in wrt if it.bc[k].dtype == T.F32} | set(extra)
 
     def prop(eqns):
-        for e in eqns:
-            if e.prim in ("emit", "threefry", "bits", "uniform01", "inrange", "floor", "round", "stop", "gather") \
-                    or not e.outs:
-                continue
-            if e.prim == "while" and _uses([e]) & act or any(isinstance(x, T.Var) and x.id in act for x in e.ins):
-                for o in e.outs:
-                    if o.dtype == T.F32:
-                        act.add(o.id)
+        _prop(eqns, act)
     prop(tr.pre)
     carry_act = [isinstance(x, T.Var) and x.id in act for x in tr.carry_in]
     while True:
@@ -1017,8 +1043,7 @@ class _Rev:
         for e in reversed(eqns):
             if e.prim == "while":
                 if _uses([e]) & self.active:
-                    raise LowerError("tallymap_b200.lower: reverse mode through an inner while loop that reads a "
-                                     "differentiated value is not lowered (its iterations would need a tape)")
+                    self.while_t(e, names, ct_tally)
                 continue
             if e.prim == "spawn":
                 if self.spawn_t is not None:
@@ -1039,6 +1064,84 @@ class _Rev:
             if not e.outs or e.outs[0].id not in self.ct:
                 continue
             self.rule(e, self.ct[e.outs[0].id], [_ref(x, names) for x in e.ins], names)
+
+    def _acc(self, xid):
+        """the cotangent local of outer value xid, declared (zero) here if it has none yet: an inner loop adds into
+        it from inside its own scopes"""
+        if xid not in self.ct:
+            self.n += 1
+            nm = f"{self.tag}{xid}_{self.n}"
+            self.lines.append(f"{self.indent}float {nm} = 0.0f;")
+            self.ct[xid] = nm
+        return self.ct[xid]
+
+    def while_t(self, e, names, ct_tally):
+        """the transpose of an inner loop that reads a differentiated value (the reference differentiates every
+        loop, _reverse.py:1-25): its trip count K by running it from its initial carry, then its iterations newest
+        first -- each one's starting state recomputed from the initial carry (no tape: K(K-1)/2 body evaluations)
+        and its body's VJP applied to the carry cotangents; the values it reads from outside gather their
+        cotangents across the iterations"""
+        p = e.params
+        if any(x.prim == "append" for x in T._walk(p["body"])) and self.append_t is not None:
+            raise LowerError("tallymap_b200.lower: reverse mode through a Records append inside an inner while loop "
+                             "that reads a differentiated value is not lowered")
+        inner, cact = _inner_active(e, self.active)
+        carry, ind = p["carry"], self.indent
+        self.n += 1
+        u = f"{self.tag}w{self.n}_"
+        clos = sorted((_uses(p["body"]) | _ids(p["body_out"])) - _defs_deep(p["body"]) - _ids(carry))
+        outer = [xid for xid in clos if xid in self.active]
+        outer += [x.id for x, a_ in zip(e.ins, cact) if a_ and isinstance(x, T.Var) and x.id in self.active]
+        for xid in dict.fromkeys(outer):
+            self._acc(xid)
+        ins_c = [_ref(x, names) for x in e.ins]
+        L = self.lines
+
+        def state(prefix, nm, indent):
+            for j, (cv, x) in enumerate(zip(carry, ins_c)):
+                L.append(f"{indent}{CTYPE[cv.dtype]} {prefix}{j} = {x};")
+                nm[cv.id] = f"{prefix}{j}"
+
+        def step(prefix, nm, indent):
+            L.extend(_emit_code(p["body"], nm, None, indent, skip_emits=True))
+            L.extend(f"{indent}const {CTYPE[cv.dtype]} {prefix}n{j} = {_ref(b, nm)};"
+                     for j, (cv, b) in enumerate(zip(carry, p["body_out"])))
+            L.extend(f"{indent}{prefix}{j} = {prefix}n{j};" for j in range(len(carry)))
+        L.append(f"{ind}{{")
+        i2, i3 = ind + "  ", ind + "    "
+        nm = dict(names)
+        state(u + "s", nm, i2)
+        L.append(f"{i2}int {u}K = 0;")
+        L.append(f"{i2}while (true) {{")
+        L.extend(_emit_code(p["cond"], nm, None, i3, skip_emits=True))
+        L.append(f"{i3}if (!({_ref(p['cond_out'], nm)})) break;")
+        step(u + "s", nm, i3)
+        L.append(f"{i3}++{u}K;")
+        L.append(f"{i2}}}")
+        for j, o in enumerate(e.outs):
+            if cact[j]:
+                L.append(f"{i2}float {u}c{j} = {self.ct.get(o.id, '0.0f')};")
+        L.append(f"{i2}for (int {u}i = {u}K - 1; {u}i >= 0; --{u}i) {{")
+        nm = dict(names)
+        state(u + "r", nm, i3)
+        L.append(f"{i3}for (int {u}q = 0; {u}q < {u}i; ++{u}q) {{")
+        step(u + "r", dict(nm), i3 + "  ")
+        L.append(f"{i3}}}")
+        L.extend(_emit_code(p["body"], nm, None, i3, skip_emits=True))
+        sub = _Rev(inner, indent=i3, tag=u + "g")
+        for xid in dict.fromkeys(outer):
+            sub.ct[xid] = self.ct[xid]
+        for j, b in enumerate(p["body_out"]):
+            if cact[j]:
+                sub.add(b, f"{u}c{j}")
+        sub.run(p["body"], nm, ct_tally)
+        L.extend(sub.lines)
+        L.extend(f"{i3}{u}c{j} = {sub.ct.get(cv.id, '0.0f')};" for j, cv in enumerate(carry) if cact[j])
+        L.append(f"{i2}}}")
+        for j, x in enumerate(e.ins):
+            if cact[j] and isinstance(x, T.Var) and x.id in self.active:
+                L.append(f"{i2}{self.ct[x.id]} = {self.ct[x.id]} + {u}c{j};")
+        L.append(f"{ind}}}")
 
     def rule(self, e, g, a, names):
         p, x = e.prim, e.ins
@@ -1917,12 +2020,40 @@ def _emit_code_jvp(eqns, names, tnames, act, L, emitter, temitter, indent="    "
     for e in eqns:
         a = [names[x.id] if isinstance(x, T.Var) else c_lit(x) for x in e.ins]
         if e.prim == "while":
-            if _uses([e]) & (set(act) | set(tnames)):
-                raise LowerError("tallymap_b200.lower: forward mode through an inner while loop that reads a "
-                                 "differentiated value is not lowered")
-            # (no tangent inside: the loop as the forward runs it; its appends carry zero field tangents)
-            app = None if appender is None else (lambda rn, w, vals: appender(rn, w, vals, [None] * len(vals)))
-            out += _emit_code([e], names, emitter, indent, appender=app)
+            act_s = set(act) | set(tnames)
+            if not _uses([e]) & act_s:
+                # (no tangent inside: the loop as the forward runs it; its appends carry zero field tangents)
+                app = None if appender is None else (lambda rn, w, vals: appender(rn, w, vals, [None] * len(vals)))
+                out += _emit_code([e], names, emitter, indent, appender=app)
+                continue
+            # forward mode through the loop: each active float carry's L tangents carried beside it
+            p = e.params
+            inner, cact = _inner_active(e, act_s)
+            tn = dict(tnames)
+            for j, (cv, o, x) in enumerate(zip(p["carry"], e.outs, e.ins)):
+                out.append(f"{indent}{CTYPE[o.dtype]} v{o.id} = {a[j]};")
+                names[o.id] = names[cv.id] = f"v{o.id}"
+                if cact[j]:
+                    t0 = tnames.get(x.id) if isinstance(x, T.Var) else None
+                    out += [f"{indent}float dv{o.id}_{l} = {t0[l] if t0 else '0.0f'};" for l in range(L)]
+                    tn[cv.id] = [f"dv{o.id}_{l}" for l in range(L)]
+            out.append(f"{indent}while (true) {{")
+            out += _emit_code(p["cond"], names, None, indent + "  ")
+            out.append(f"{indent}  if (!({_ref(p['cond_out'], names)})) break;")
+            out += _emit_code_jvp(p["body"], names, tn, inner, L, emitter, temitter, indent + "  ", spawner, appender)
+            for j, (o, b) in enumerate(zip(e.outs, p["body_out"])):
+                out.append(f"{indent}  const {CTYPE[o.dtype]} n{o.id} = {_ref(b, names)};")
+                if cact[j]:
+                    bt = tn.get(b.id) if isinstance(b, T.Var) else None
+                    out += [f"{indent}  const float nd{o.id}_{l} = {bt[l] if bt else '0.0f'};" for l in range(L)]
+            for j, o in enumerate(e.outs):
+                out.append(f"{indent}  v{o.id} = n{o.id};")
+                if cact[j]:
+                    out += [f"{indent}  dv{o.id}_{l} = nd{o.id}_{l};" for l in range(L)]
+            out.append(f"{indent}}}")
+            for j, o in enumerate(e.outs):
+                if cact[j]:
+                    tnames[o.id] = [f"dv{o.id}_{l}" for l in range(L)]
             continue
         if e.prim == "spawn":
             if spawner is not None:

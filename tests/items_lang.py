@@ -567,3 +567,20 @@ def rejection_active(t, x, key, a):
         return k + 1, x + 0.1, t.add("h", 0, y)
     k, x, t = tl.while_loop(lambda c: c[0] < 5, body, (0, x, t))
     return t, k
+
+
+def newton(t, x, key, a):
+    """each step runs 3 + k % 4 fixed-point iterations y <- x + a sin(y) (an inner loop whose carry and body read the
+    differentiated a and the step's x, adding a * y to bin 1 at every iterate), adds the result to bin 0 and moves
+    x by 0.1 y: an active stepping carry and an active inner loop, smooth in a"""
+    def body(c):
+        k, x, t = c
+
+        def it(d):
+            j, y, t = d
+            y2 = x + a * tl.sin(y)
+            return j + 1, y2, t.add("h", 1, a * y2)
+        j, y, t = tl.while_loop(lambda d: d[0] < 3 + k % 4, it, (0, x, t))
+        return k + 1, x + 0.1 * y, t.add("h", 0, y)
+    k, x, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
+    return t, k

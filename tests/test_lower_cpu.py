@@ -1037,10 +1037,10 @@ def test_inner_while_loops():
     """inner while loops -- inside the stepping loop's body (reading the step's key from outside, writing the tally
     inside), inside a cond branch (iterating only where the branch is taken), after the stepping loop, and a
     fori_loop with a traced bound -- trace to nested "while" equations that the IR evaluator runs as the host
-    restatement does, bitwise; the forward, reverse, one-pass and forward-mode programs compile when the inner loops
-    read no differentiated value, and reverse / forward mode refuse one that does"""
+    restatement does, bitwise; the forward, reverse, one-pass and forward-mode programs compile, inner loops that
+    read a differentiated value included"""
     from oracle.ir_eval import Evaluator
-    from items_lang import rejection, rejection_active
+    from items_lang import newton, rejection, rejection_active
     specs = {"h": ((9,), "f32"), "tries": ((2,), "i32")}
     tr = T.trace_item(rejection, ["f32", "key", "f32"], 2, specs)
     assert sum(e.prim == "while" for e in tr.body) == 2 and sum(e.prim == "while" for e in tr.post) == 2
@@ -1064,10 +1064,11 @@ def test_inner_while_loops():
     assert src.count("while (true)") >= 4
     assert L.grad_program((0,)).kernel > 0 and L.jvp_program((0,), 1).kernel > 0
     assert L.vg_program((0,)).kernel > 0
-    g = tm.vmap(rejection_active, outputs={"h": tm.Sum((1,))}, in_axes=(0, 0, None), max_steps=10)
-    La = g.lowered((x0, keys, a))
-    assert La.fwd.kernel > 0
-    with pytest.raises(tm.UnsupportedError, match="inner while loop"):
-        La.grad_program((0,))
-    with pytest.raises(tm.UnsupportedError, match="inner while loop"):
-        La.jvp_program((0,), 1)
+    # inner loops that read the differentiated value: reverse mode transposes them (trip count, then the iterations
+    # newest first from recomputed states), forward mode carries their tangents
+    for item in (rejection_active, newton):
+        g = tm.vmap(item, outputs={"h": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=10)
+        La = g.lowered((x0, keys, a))
+        assert La.fwd.kernel > 0 and La.grad_program((0,)).kernel > 0 and La.jvp_program((0,), 2).kernel > 0
+        assert La.vg_program((0,)).kernel > 0
+        assert "for (int gw" in lower.grad_source(La.it, [0])[0]

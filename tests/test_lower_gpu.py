@@ -1027,3 +1027,47 @@ def test_inner_while_loops(cuda):
     torch.cuda.synchronize()
     assert abs(float(g) - want) <= 1e-5 * abs(want) and abs(float(gv) - want) <= 1e-5 * abs(want)
     assert near(d["h"].cpu().numpy(), ref["sums"]["h"] / float(a))
+
+
+@pytest.mark.parametrize("name", ["newton", "rejection_active"])
+def test_inner_while_loops_differentiated(cuda, name):
+    """inner loops that read the differentiated a (newton: fixed-point iterations of y = x + a sin y, whose iterates
+    write the tally, under an active stepping carry; rejection_active: a loop whose trip count and carry depend on a):
+    the replay gradient (the inner loop transposed from recomputed states), the forward-mode value-and-grad and jvp
+    agree within 1e-5; newton's with a central difference of the IR evaluator within 1e-3, rejection_active's with the
+    host count of its trip counts (its derivative, the trip counts being locally constant) within 1e-5"""
+    import items_lang
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as Tr
+    item = getattr(items_lang, name)
+    n = 2000
+    x0 = np.random.default_rng(9).uniform(0.1, 0.6, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(3), n)
+    a, h = 0.35, 1e-3
+    ct = torch.tensor([0.7, -1.3])
+    f = tm.vmap(item, outputs={"h": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=10)
+    g = float(f.grad(x0, keys, np.float32(a), wrt=2, cotangents={"h": ct}))
+    _, gv = f.value_and_grad(x0, keys, np.float32(a), wrt=2, cotangents={"h": ct})
+    _, d = f.jvp(x0, keys, np.float32(a), wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    gj = float(np.dot(ct.numpy().astype(np.float64), d["h"].cpu().numpy()))
+    assert abs(g - float(gv)) <= 1e-5 * abs(g) and abs(g - gj) <= 1e-5 * abs(g)
+    if name == "newton":
+        tr = Tr.trace_item(item, ["f32", "key", "f32"], 2, {"h": ((2,), "f32")})
+        q = lambda aa: Evaluator(tr, 10).run([x0, keys], [np.float32(aa)])["sums"]["h"]
+        want = float(np.dot(ct.numpy().astype(np.float64), (q(a + h) - q(a - h)) / (2 * h)))
+        assert abs(g - want) <= 1e-3 * abs(want), (g, want)
+        return
+    # rejection_active: y = x + m a after m iterations (a trip count that steps with a): d h[0] / d a = the sum of
+    # the trip counts, counted on the host in float32
+    f32, m_all = np.float32, 0
+    for x in x0:
+        x = f32(x)
+        for _ in range(5):
+            y, m = x, 0
+            while m < 4 and y < 1.0:
+                y, m = f32(y + f32(a)), m + 1
+            m_all += m
+            x = f32(x + f32(0.1))
+    want = float(ct[0]) * m_all
+    assert abs(g - want) <= 1e-5 * abs(want), (g, want)
