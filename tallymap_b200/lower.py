@@ -1021,11 +1021,12 @@ class _Rev:
     """reverse-mode code for a straight-line equation list: cotangent locals, first contribution assigned, later ones
     added (jax's add_jaxvals order)"""
 
-    def __init__(self, active, indent="    ", tag="g", spawn_t=None, append_t=None):
+    def __init__(self, active, indent="    ", tag="g", spawn_t=None, append_t=None, append_skip=None):
         self.active, self.ct, self.lines, self.indent, self.tag = active, {}, [], indent, tag
         self.n = 0
         self.spawn_t = spawn_t      # the transpose of a spawn (the tree adjoint), else spawns have no cotangent
         self.append_t = append_t    # the transpose of a Records append, else appends have no cotangent
+        self.append_skip = append_skip  # (records, when, fields) -> C: an append without a cotangent, counted
 
     def add(self, x, expr):
         if not isinstance(x, T.Var) or x.id not in self.active:
@@ -1044,6 +1045,13 @@ class _Rev:
             if e.prim == "while":
                 if _uses([e]) & self.active:
                     self.while_t(e, names, ct_tally)
+                elif self.append_skip is not None and any(x.prim == "append" for x in T._walk(e.params["body"])):
+                    # (the loop's records have no cotangent, but each one moves the append ordinal at which the
+                    # adjoint reads the earlier records' cotangents: the loop re-run, counting them)
+                    self.lines.append(f"{self.indent}{{")
+                    self.lines += _emit_code([e], dict(names), None, self.indent + "  ", skip_emits=True,
+                                             appender=self.append_skip)
+                    self.lines.append(f"{self.indent}}}")
                 continue
             if e.prim == "spawn":
                 if self.spawn_t is not None:
@@ -1082,9 +1090,6 @@ class _Rev:
         and its body's VJP applied to the carry cotangents; the values it reads from outside gather their
         cotangents across the iterations"""
         p = e.params
-        if any(x.prim == "append" for x in T._walk(p["body"])) and self.append_t is not None:
-            raise LowerError("tallymap_b200.lower: reverse mode through a Records append inside an inner while loop "
-                             "that reads a differentiated value is not lowered")
         inner, cact = _inner_active(e, self.active)
         carry, ind = p["carry"], self.indent
         self.n += 1
@@ -1128,7 +1133,8 @@ class _Rev:
         step(u + "r", dict(nm), i3 + "  ")
         L.append(f"{i3}}}")
         L.extend(_emit_code(p["body"], nm, None, i3, skip_emits=True))
-        sub = _Rev(inner, indent=i3, tag=u + "g")
+        # (a Records append inside: transposed per iteration, newest first, as the forward appended them)
+        sub = _Rev(inner, indent=i3, tag=u + "g", append_t=self.append_t, append_skip=self.append_skip)
         for xid in dict.fromkeys(outer):
             sub.ct[xid] = self.ct[xid]
         for j, b in enumerate(p["body_out"]):
@@ -1457,6 +1463,9 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     nsp = [0]
     nap = [0]
 
+    def append_skip(rname, when_c, vals_c):
+        return f"if ({when_c}) a.ka{rindex[rname]} -= 1;"
+
     def append_t(rev, e, names):
         """a Records append's transpose: its float fields' cotangents from the canonical slot offset + k"""
         nap[0] += 1
@@ -1529,7 +1538,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  __device__ __forceinline__ static void vjp(const Ctx& c, const State& at, Adj& a) {")
     names = _names_loop(it, tr.carry, "at")
     lines += _emit_code(tr.body, names, None, skip_emits=True)
-    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None,
+               append_skip=append_skip if recs else None)
     for j, x in enumerate(tr.body_out):
         if carry_act[j]:
             rev.add(x, f"a.cc{j}")
@@ -1541,7 +1551,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
     lines.append("  __device__ static void post_vjp(const Ctx& c, const State& fin, Adj& a) {")
     names = _names_loop(it, tr.post_carry, "fin")
     lines += _emit_code(tr.post, names, None, skip_emits=True)
-    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None)
+    rev = _Rev(act, spawn_t=spawn_t if tree else None, append_t=append_t if recs else None,
+               append_skip=append_skip if recs else None)
     rev.run(tr.post, names, ct_tally)
     lines += rev.lines
     lines += finish_rev(rev, tr.post_carry, True, "pb")
@@ -1557,7 +1568,8 @@ def grad_source(it, wrt, standalone=True, wrt_pi=(), tree=False):
         for v, ld in it.loads:
             lines.append(f"    const {CTYPE[v.dtype]} v{v.id} = {ld};")
     lines += _emit_code(tr.pre, names, None, skip_emits=True)
-    rev = _Rev(act, tag="h", append_t=append_t if recs else None)
+    rev = _Rev(act, tag="h", append_t=append_t if recs else None,
+               append_skip=append_skip if recs else None)
     for j, x in enumerate(tr.carry_in):
         if carry_act[j]:
             rev.add(x, f"a.cc{j}")

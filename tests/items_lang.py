@@ -584,3 +584,22 @@ def newton(t, x, key, a):
         return k + 1, x + 0.1 * y, t.add("h", 0, y)
     k, x, t = tl.while_loop(lambda c: c[0] < 6, body, (0, x, t))
     return t, k
+
+
+def loop_records(t, x, key, a):
+    """Records appended inside inner loops: each step iterates y <- 0.5 y + x for 1 + k % 3 iterations, appending
+    {"v": a y} at each (a loop that reads the differentiated a: its appends are transposed iteration by iteration),
+    then a loop that reads no differentiated value appends {"v": x} twice (no cotangent, but it moves the append
+    ordinal), and adds a y to the Sum"""
+    def body(c):
+        k, x, t = c
+
+        def it(d):
+            j, y, t = d
+            y = 0.5 * y + x
+            return j + 1, y, t.append("r", {"v": a * y})
+        j, y, t = tl.while_loop(lambda d: d[0] < 1 + k % 3, it, (0, x, t))
+        j2, t = tl.while_loop(lambda d: d[0] < 2, lambda d: (d[0] + 1, d[1].append("r", {"v": x})), (0, t))
+        return k + 1, x + 0.1, t.add("h", 0, a * y)
+    k, x, t = tl.while_loop(lambda c: c[0] < 4, body, (0, x, t))
+    return t, k

@@ -217,3 +217,34 @@ def test_count_then_fill_with_an_overflowing_capacity_output(cuda):
     assert torch.isnan(r.outputs["last"]["w"]).all() and (r.outputs["last"]["k"] == -1).all()
     assert torch.isnan(r.outputs["tot"])
     assert int(r.stats["records_mismatch"]["hits"]) == 0
+
+
+@pytest.mark.parametrize("cap", [1 << 15, None])
+def test_records_inside_inner_loops(cuda, cap):
+    """Records appended inside inner loops (items_lang.loop_records): the canonical records bitwise the IR
+    evaluator's; the adjoint -- the loop that reads a transposed iteration by iteration, the other re-run to count its
+    appends -- against the jvp's contraction within 1e-5; one pass (a capacity) and count-then-fill alike"""
+    from items_lang import loop_records
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as T
+    n = 1000
+    x = np.random.default_rng(4).uniform(0.2, 0.9, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(6), n)
+    a = np.float32(0.8)
+    outs = {"h": tm.Sum((1,)), "r": tm.Records({"v": torch.float32}, capacity=cap)}
+    f = tm.vmap(loop_records, outputs=outs, in_axes=(0, 0, None), max_steps=8)
+    tr = T.trace_item(loop_records, ["f32", "key", "f32"], 2, {"h": ((1,), "f32")}, {"r": (1 << 15, (("v", "f32"),))})
+    ref = Evaluator(tr, 8).run([x, keys], [a])
+    want_v = np.array([rec[0] for rec in ref["records"]["r"]], np.float32)
+    m = len(want_v)
+    r = f(x, keys, a)
+    torch.cuda.synchronize()
+    assert m == 15 * n and int(r.stats["appended"]["r"]) == m
+    assert np.array_equal(r.outputs["r"]["v"].cpu().numpy()[:m].view(np.uint32), want_v.view(np.uint32))
+    ctv = torch.from_numpy(np.random.default_rng(7).normal(size=cap or m).astype(np.float32))
+    ct = {"h": torch.tensor([0.4]), "r": {"v": ctv}}
+    g = f.grad(x, keys, a, wrt=2, cotangents=ct)
+    _, d = f.jvp(x, keys, a, wrt=2, tangents=[1.0])
+    torch.cuda.synchronize()
+    want = 0.4 * float(d["h"][0]) + float((ctv.double() * d["r"]["v"].cpu().double()).sum())
+    assert abs(float(g) - want) <= 1e-5 * abs(want)
