@@ -212,8 +212,12 @@ def _lit(x):
 class Evaluator:
     """evaluate traced item `tr` over items: run(per_item operands, broadcast values) -> dict of outputs"""
 
-    def __init__(self, tr, max_steps, exact=(), max_items=10 ** 7):
+    def __init__(self, tr, max_steps, exact=(), max_items=10 ** 7, wide=None):
+        """wide: {output: (dtype "f64" | "i32" | "i64", scale)} -- the scaled fixed-point Sums (tallymap/_api.py:55-84),
+        kept as exact Python integers sum(round(v * scale)) and read out as float(total) / scale, float(int) being
+        the correctly rounded double of the exact total, then the output's type (toward zero for an integer)"""
         self.tr, self.M, self.exact, self.max_items = tr, int(max_steps), set(exact), max_items
+        self.wide = dict(wide or {})
 
     def _val(self, x, env):
         return env[x.id] if isinstance(x, T.Var) else _lit(x)
@@ -267,6 +271,8 @@ class Evaluator:
         specs = tr.specs
         sums = {}
         exact_pairs = {nm: ([], []) for nm in self.exact}
+        wide_tot = {nm: [0] * (int(np.prod(specs[nm][0])) if specs[nm][0] else 1) for nm in self.wide}
+        wide_flag = {nm: [False] * len(wide_tot[nm]) for nm in self.wide}
         for nm, (shape, dt) in specs.items():
             S = int(np.prod(shape)) if shape else 1
             sums[nm] = np.zeros(S, np.float64 if dt == T.F32 else np.int64)
@@ -340,6 +346,13 @@ class Evaluator:
                 elif nm in self.exact:
                     exact_pairs[nm][0].append(v)
                     exact_pairs[nm][1].append(idx)
+                elif nm in self.wide:
+                    x = float(v) * float(self.wide[nm][1])
+                    if not abs(x) < 9.2e18:
+                        stats[3] += 1
+                        wide_flag[nm][idx] = True
+                    else:
+                        wide_tot[nm][idx] += round(x)
                 else:
                     sums[nm][idx] += float(v) if specs[nm][1] == T.F32 else int(v)
             for nm, fields in out["appends"]:
@@ -347,4 +360,18 @@ class Evaluator:
                 counts[nm][i] += 1
         for nm, (vals, bins) in exact_pairs.items():
             sums[nm] = orc.exact_sum(np.array(vals, np.float32), np.array(bins, np.int32), len(sums[nm]))[0]
+        for nm, (dt, scale) in self.wide.items():
+            vals = []
+            for tot, flag in zip(wide_tot[nm], wide_flag[nm]):
+                v = float(tot) * (1.0 / float(scale))
+                if dt == "f64":
+                    big = not abs(v) <= 1.7976931348623157e308
+                    stats[3] += int(big and not flag)
+                    vals.append(math.nan if flag or big else v)
+                else:
+                    lim = 2 ** 63 if dt == "i64" else 2 ** 31
+                    stats[3] += int(not -lim <= v < lim)
+                    # (the device's conversion toward zero saturates)
+                    vals.append(0 if v != v else lim - 1 if v >= lim else -lim if v < -lim else int(v))
+            sums[nm] = np.array(vals, np.float64 if dt == "f64" else np.int64)
         return dict(sums=sums, records=records, counts=counts, stats=stats, results=results, trunc=trunc)

@@ -31,19 +31,38 @@ from .trace import TallyError, UnsupportedError  # noqa: F401  (the reference's 
 
 @dataclasses.dataclass(frozen=True)
 class Sum:
-    """a summed output of a fixed shape (tallymap.Sum, _api.py:55-84).  fixed_point=True (float32, items traced from
-    Python functions): EXACT -- each bin is the correctly rounded float32 of the exact sum of its emits, bitwise
-    independent of their order (run to run, launch order, number of GPUs); a non-finite emit or an accumulator
-    overflow makes the bin NaN, counted in stats['fixed_point_overflow']."""
+    """a summed output of a fixed shape (tallymap.Sum, _api.py:55-84), of dtype float32, int32, float64 or int64 (a
+    float64 output sums the item's float32 values in float64, an int64 one its int32 values in int64).
+    fixed_point=True with float32 (items traced from Python functions): EXACT -- each bin is the correctly rounded
+    float32 of the exact sum of its emits, bitwise independent of their order (run to run, launch order, number of
+    GPUs); a non-finite emit or an accumulator overflow makes the bin NaN, counted in stats['fixed_point_overflow'].
+    fixed_point=True with another dtype: each emit adds round(v * scale) to an int64 word whose signed carry is kept
+    beside it, so a bin's total is exact and order-independent past 2^63; it is read out as total / scale in the
+    output's dtype.  An emit with |v * scale| >= 9.2e18 is dropped, counted in 'fixed_point_overflow', and makes a
+    float bin NaN; a total that does not fit the dtype is counted there too (a float bin is NaN)."""
     shape: tuple
     dtype: torch.dtype = torch.float32
     fixed_point: bool = False
+    scale: float = 2.0 ** 32
 
     def __post_init__(self):
         shape = (self.shape,) if isinstance(self.shape, (int, np.integer)) else self.shape
         object.__setattr__(self, "shape", tuple(int(s) for s in shape))
+        if self.dtype not in (torch.float32, torch.int32, torch.float64, torch.int64):
+            raise TypeError("tallymap_b200: a Sum of float32, int32, float64 or int64")
+        if not (float(self.scale) > 0.0 and np.isfinite(float(self.scale))):
+            raise ValueError("tallymap_b200: a fixed-point Sum's scale is a positive finite number")
+
+    def accumulator(self):
+        """None (a plain float32 / int32 sum, or the exact float32 one), ("f64",), ("i64",) or ("wide", dtype,
+        scale) (the scaled fixed-point sum)"""
         if self.fixed_point and self.dtype != torch.float32:
-            raise NotImplementedError("tallymap_b200: fixed_point Sums of float32 only (the exact accumulator)")
+            return ("wide", self.dtype, float(self.scale))
+        if self.dtype == torch.float64:
+            return ("f64",)
+        if self.dtype == torch.int64:
+            return ("i64",)
+        return None
 
 
 @dataclasses.dataclass(frozen=True)
@@ -148,6 +167,11 @@ def _limits(p, stats):
     if p.spawns:
         bad = bad | (stats["children_dropped"] > 0) | (stats["children_truncated"] > 0)
     return bad
+
+
+def _f32(c):
+    """a cotangent as float32 (a float64 output's cotangent enters the float32 adjoint)"""
+    return c.to(torch.float32) if isinstance(c, torch.Tensor) and c.dtype != torch.float32 else c
 
 
 def _poison(outs, bad):
@@ -387,10 +411,10 @@ class MappedFn:
                 self.outputs[name] = ("records", o.capacity,
                                       tuple((f, "f32" if dt == torch.float32 else "i32") for f, dt in o.fields))
                 continue
-            if o.dtype not in (torch.float32, torch.int32):
-                raise TypeError(f"tallymap_b200: output {name!r}: Sum of float32 or int32")
-            self.outputs[name] = (tuple(o.shape), "f32" if o.dtype == torch.float32 else "i32",
-                                  bool(getattr(o, "fixed_point", False)))
+            # (shape, the item's value type, exact float32 sum, the wider accumulator or None)
+            acc = o.accumulator()
+            self.outputs[name] = (tuple(o.shape), "f32" if o.dtype in (torch.float32, torch.float64) else "i32",
+                                  bool(o.fixed_point) and o.dtype == torch.float32, acc)
         if in_axes == 0:
             import inspect
             ps = list(inspect.signature(fn).parameters.values())[1:]
@@ -634,7 +658,7 @@ class MappedFn:
             if o[0] == "records" or o[1] != "f32":
                 continue
             c = cotangents.get(name)
-            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else _f32(c))
         over = False
         if L.fwd.records:
             # (a Records output's cotangents sit at its canonical slots: the adjoint needs each item's record count
@@ -802,7 +826,7 @@ class MappedFn:
             if o[1] != "f32":
                 continue
             c = cotangents.get(name)
-            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else _f32(c))
         r = B.tree_adjoint(adj, t, cts, max_steps=self.max_steps, rev_checkpoints=self.opts["rev_checkpoints"])
         self.last_tree = r["info"]
         out = t["forward"]
@@ -821,7 +845,7 @@ class MappedFn:
             if o[0] == "records" or o[1] != "f32":
                 continue
             c = cotangents.get(name)
-            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else c)
+            cts.append(torch.zeros(o[0], dtype=torch.float32) if c is None else _f32(c))
         out = B.run(prog, pi, list(bc) + cts, consts=(self.max_steps,),
                     queue=self.spawn.capacity if self.spawn else None)
         nt = len(L.fwd.tallies)

@@ -39,6 +39,7 @@ class TSpec:
     dtype: torch.dtype = torch.float32
     exact: bool = False
     f64: bool = False      # accumulated in an f64 shadow (a scratch result), rounded once to the f32 output
+    wide: float = 0.0      # nonzero: a scaled fixed-point sum of this scale (lo / carry / flag words per bin)
 
     def dims(self, N=None):
         """the shape with a leading "N" (a tally indexed by item id) resolved to the launch's item count"""
@@ -107,6 +108,9 @@ class ItemProgram:
                 # EXACT_WORDS int64 words per bin, then one u32 flag word per bin (rounded up to whole u64s)
                 n64 = S * EXACT_WORDS + (S + 1) // 2
                 out.append((t.name + ".exact", n64 * 8, torch.int64, (n64,)))
+            if t.wide:
+                # per bin: an int64 low word, then an i32 carry and a u32 flag (csrc/tm_tally.cuh WideSum)
+                out.append((t.name + ".wide", S * 16, torch.int64, (2 * S,)))
         for name, cap, fields in self.records:
             # the raw records (a slot per append, in claim order), their keys (item, ordinal) and the slot counter;
             # a fill pass: the fields alone, in the canonical layout

@@ -226,4 +226,64 @@ struct SumPriv {
   }
 };
 
+// A scaled fixed-point sum (a Sum(fixed_point=True) of another dtype than float32; tallymap/_api.py:55-84): a bin
+// is an int64 word `lo` that wraps, a signed count `carry` of its wraps (+1 when an add of q > 0 left it below its old
+// value, -1 when one of q < 0 left it above), and a flag.  Whatever order the adds run in, the bin's total is exactly
+// lo + carry * 2^64.  Layout of the scratch: lo[S], then carry i32[S], then flag u32[S].
+struct WideSum {
+  // add round(x) (x = v * scale); |x| >= 9.2e18 is not representable: dropped, counted and the bin flagged
+  __device__ __forceinline__ static void emit(unsigned long long* lo, i32* carry, u32* flag, i32* stats, i32 b,
+                                              double x) {
+    if (!(fabs(x) < 9.2e18)) {
+      atomicAdd(&stats[kStFixedPointOverflow], 1);
+      flag[b] = 1u;
+      return;
+    }
+    const long long q = __double2ll_rn(x);
+    if (q == 0) return;
+    const long long before = (long long)atomicAdd(&lo[b], (unsigned long long)q);
+    const long long after = (long long)((unsigned long long)before + (unsigned long long)q);
+    if (q > 0 && after < before) atomicAdd(&carry[b], 1);
+    if (q < 0 && after > before) atomicAdd(&carry[b], -1);
+  }
+  // the 128-bit integer lo + carry * 2^64 rounded once to double: its magnitude split into high and low 64-bit
+  // halves, the top 64 significant bits converted by the hardware's round-to-nearest-even with every bit below them
+  // folded into the lowest one (a sticky bit: it decides a tie the way the full value does), then scaled by 2^shift
+  __device__ static double total(unsigned long long lo, i32 carry) {
+    if (carry == 0) return (double)(long long)lo;
+    unsigned long long hi = (unsigned long long)((long long)carry + ((long long)lo < 0 ? -1ll : 0ll));
+    unsigned long long low = lo;
+    const bool neg = (long long)hi < 0;
+    if (neg) {                                         // the magnitude: two's complement negation of hi:low
+      low = ~low + 1ull;
+      hi = ~hi + (low == 0ull ? 1ull : 0ull);
+    }
+    if (hi == 0ull) return neg ? -(double)low : (double)low;
+    const int bits = 64 - __clzll((long long)hi);      // significant bits of hi: the magnitude has 64 + bits
+    const unsigned long long top = bits == 64 ? hi : ((hi << (64 - bits)) | (low >> bits));
+    const unsigned long long below = bits == 64 ? low : (low << (64 - bits));
+    const double m = ldexp((double)(top | (below != 0ull ? 1ull : 0ull)), bits);
+    return neg ? -m : m;
+  }
+  // readout into the output (once per launch, after every emit): total / scale in the output's type; a flagged
+  // bin is NaN in a float output; a value outside the output's range counts in fixed_point_overflow (a float bin
+  // NaN, an integer bin saturated by the conversion)
+  template <class O>
+  __device__ static void readout(const unsigned long long* lo, const i32* carry, const u32* flag, O* out, i64 S,
+                                 double inv_scale, i32* stats, int tid, int nth) {
+    for (i64 i = tid; i < S; i += nth) {
+      const double v = total(lo[i], carry[i]) * inv_scale;
+      if (sizeof(O) == 8 && (O)0.5 != (O)0) {          // double
+        const bool big = !(fabs(v) <= 1.7976931348623157e308);
+        if (big && !flag[i]) atomicAdd(&stats[kStFixedPointOverflow], 1);
+        out[i] = (flag[i] || big) ? (O)__longlong_as_double(0x7ff8000000000000ll) : (O)v;
+      } else {
+        const double lim = sizeof(O) == 8 ? 9223372036854775808.0 : 2147483648.0;
+        if (!(v >= -lim && v < lim)) atomicAdd(&stats[kStFixedPointOverflow], 1);
+        out[i] = (O)v;
+      }
+    }
+  }
+};
+
 }  // namespace tmb

@@ -253,9 +253,11 @@ def _defs(eqns):
 class Item:
     """the layout facts of a traced item shared by its forward and reverse lowering"""
 
-    def __init__(self, tr, in_specs, name, exact=()):
+    def __init__(self, tr, in_specs, name, exact=(), acc=None):
         self.tr, self.name = tr, name
         self.exact = set(exact)                 # Sum(fixed_point=True) f32 outputs: exact bins
+        # the wider accumulators: name -> ("f64",) | ("i64",) | ("wide", torch dtype, scale)
+        self.acc = dict(acc or {})
         self.in_specs = list(in_specs)
         npi = tr.n_per_item
         self.pi = tr.inputs[:npi]
@@ -469,6 +471,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     for t, (name, _) in enumerate(it.specs):
         if name in it.exact:
             enum.append(f"kX{t} = {idx}"); idx += 1
+        elif it.acc.get(name, ("",))[0] == "wide":
+            enum.append(f"kW{t} = {idx}"); idx += 1
     for r, (rname, (cap, fields)) in enumerate(recs):
         if count:
             continue
@@ -515,7 +519,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
         nbytes = S * 44 if name in it.exact else S * 4
-        if nbytes <= (4 * PRIV_BYTES if name in it.exact else PRIV_BYTES):
+        if name not in it.acc and nbytes <= (4 * PRIV_BYTES if name in it.exact else PRIV_BYTES):
             priv[name] = (t, smem, S, dt)
             smem += (nbytes + 15) // 16 * 16
     lines.append(f"  static constexpr int kSmemBytes = {max(smem, 16)};")
@@ -530,7 +534,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     tinfo = {}
     for t, (name, (shape, dt)) in enumerate(it.specs):
         S = int(np.prod(shape, dtype=np.int64)) if shape else 1
-        ct = "float" if dt == T.F32 else "i32"
+        ct = _out_ctype(it, name, dt)
         ctx.append(f"    {ct}* g{t};")
         if name in it.exact:
             ctx.append(f"    u64* x{t};")
@@ -538,6 +542,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
                 ctx.append(f"    u64* sx{t};")
         elif name in priv:
             ctx.append(f"    {ct}* s{t};")
+        elif it.acc.get(name, ("",))[0] == "wide":
+            ctx.append(f"    unsigned long long* w{t};")
         tinfo[name] = (t, S, dt, name in priv)
     for r, y in enumerate(tr.results):
         ctx.append(f"    {CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}* y{r};")
@@ -580,7 +586,7 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     lines.append("    c.M = __ldg(static_cast<const i32*>(P.p[kConsts]));")
     lines.append("    c.stats = static_cast<i32*>(P.p[kStats]);")
     for name, (t, S, dt, pv) in tinfo.items():
-        ct = "float" if dt == T.F32 else "i32"
+        ct = _out_ctype(it, name, dt)
         lines.append(f"    c.g{t} = static_cast<{ct}*>(P.p[kT{t}]);")
         if name in it.exact:
             lines.append(f"    c.x{t} = static_cast<u64*>(P.p[kX{t}]);")
@@ -588,6 +594,8 @@ def forward_source(it, standalone=True, record=False, mode="one"):
                 lines.append(f"    c.sx{t} = reinterpret_cast<u64*>(smem + {priv[name][1]});")
         elif pv:
             lines.append(f"    c.s{t} = reinterpret_cast<{ct}*>(smem + {priv[name][1]});")
+        elif it.acc.get(name, ("",))[0] == "wide":
+            lines.append(f"    c.w{t} = static_cast<unsigned long long*>(P.p[kW{t}]);")
     for r, y in enumerate(tr.results):
         lines.append(f"    c.y{r} = static_cast<{CTYPE[y.dtype] if y.dtype != T.BOOL else 'uint8_t'}*>(P.p[kY{r}]);")
     lines.append("    c.trunc = static_cast<uint8_t*>(P.p[kTrunc]);")
@@ -648,6 +656,16 @@ def forward_source(it, standalone=True, record=False, mode="one"):
 
     def emitter(name, idx_c, v_c):
         t, S, dt, pv = tinfo[name]
+        acc = it.acc.get(name)
+        if acc is not None:
+            drop = f"const i32 b_ = {idx_c}; if ((u32)b_ >= {S}u) atomicAdd(&c.stats[kStDroppedEmits], 1); else"
+            if acc[0] == "f64":
+                return f"{{ {drop} if ({v_c}) atomicAdd(&c.g{t}[b_], (double)({v_c})); }}"
+            if acc[0] == "i64":
+                return (f"{{ {drop} if ({v_c}) atomicAdd((unsigned long long*)&c.g{t}[b_], "
+                        f"(unsigned long long)(long long)({v_c})); }}")
+            return (f"{{ {drop} WideSum::emit(c.w{t}, (i32*)(c.w{t} + {S}), (u32*)(c.w{t} + {S}) + {S}, c.stats, "
+                    f"b_, (double)({v_c}) * {float(acc[2])!r}); }}")
         if name in it.exact:
             return f"ExactSum<{S}>::emit({'c.sx' if pv else 'c.x'}{t}, c.stats, {idx_c}, {v_c});"
         if dt == T.F32:
@@ -782,6 +800,10 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     for name, (t, S, dt, pv) in tinfo.items():
         if name in it.exact:
             lines.append(f"    ExactSum<{S}>::readout(c.x{t}, c.g{t}, c.stats, tid, nth);")
+        elif it.acc.get(name, ("",))[0] == "wide":
+            inv = 1.0 / float(it.acc[name][2])
+            lines.append(f"    WideSum::readout(c.w{t}, (const i32*)(c.w{t} + {S}), (const u32*)(c.w{t} + {S}) + {S}, "
+                         f"c.g{t}, {S}, {inv!r}, c.stats, tid, nth);")
     lines.append("  }")
     lines.append("};")
     if not standalone:
@@ -791,6 +813,26 @@ def forward_source(it, standalone=True, record=False, mode="one"):
     lines.append(f"  tmb::{'spawn_body' if sp else 'forward_body'}<tmb::GenFwd>(P, n);")
     lines.append("}")
     return "\n".join(lines), max(smem, 16)
+
+
+def _out_dtype(it, name, dt):
+    """the torch dtype of a Sum output"""
+    acc = it.acc.get(name)
+    if acc is None:
+        return TDTYPE[dt]
+    return {"f64": torch.float64, "i64": torch.int64}.get(acc[0]) or acc[1]
+
+
+def _out_ctype(it, name, dt):
+    """the C type of a Sum output's buffer: float / i32, double / long long for the wider accumulators"""
+    acc = it.acc.get(name)
+    if acc is None:
+        return "float" if dt == T.F32 else "i32"
+    if acc[0] == "f64":
+        return "double"
+    if acc[0] == "i64":
+        return "long long"
+    return {torch.float64: "double", torch.int64: "long long", torch.int32: "i32"}[acc[1]]
 
 
 def _in_ctype(s):
@@ -1696,15 +1738,18 @@ class Lowered:
         outputs = {k: v for k, v in outputs.items() if v[0] != "records"}
         specs = {k: (tuple(v[0]), v[1]) for k, v in outputs.items()}
         exact = [k for k, v in outputs.items() if len(v) > 2 and v[2]]
+        acc = {k: v[3] for k, v in outputs.items() if len(v) > 3 and v[3]}
         self.tr = T.trace_item(fn, in_specs, n_per_item, specs, recs, spawn=spawn)
-        self.it = Item(self.tr, in_specs, self.name, exact)
+        self.it = Item(self.tr, in_specs, self.name, exact, acc)
         it = self.it
         src, smem = forward_source(it)
         self.fwd_source = src
         pi = tuple(_operand(f"in{j}", s) for j, s in enumerate(in_specs[:n_per_item]))
         bc = tuple(_operand(f"bc{k}", s) for k, s in enumerate(in_specs[n_per_item:]))
         self.pi, self.bc = pi, bc
-        tallies = tuple(TSpec(nm, shape, TDTYPE[dt], exact=nm in it.exact) for nm, (shape, dt) in it.specs)
+        tallies = tuple(TSpec(nm, shape, _out_dtype(it, nm, dt), exact=nm in it.exact,
+                              wide=float(it.acc[nm][2]) if it.acc.get(nm, ("",))[0] == "wide" else 0.0)
+                        for nm, (shape, dt) in it.specs)
         ys = tuple(_operand(f"y{r}", y.dtype) for r, y in enumerate(self.tr.results))
         ys += tuple(_operand(f"{nm}#count", T.I32) for nm in recs)
         ys += (_operand("truncated", T.BOOL),)
@@ -1712,7 +1757,7 @@ class Lowered:
         nrec = sum(len(fl) + 3 for _, _, fl in records)
         sp = it.spawns
         nbuf = len(pi) + len(bc) + 2 + len(tallies) + len(it.exact) + nrec + 2 + len(ys) + (3 if sp else 0) + \
-            int(it.claims)
+            int(it.claims) + sum(1 for t in tallies if t.wide)
         if sp:
             # the spawn runtime's shared stack entries after the item's block (csrc/tm_spawn.cuh SpawnSmem)
             smem = (smem + 15) // 16 * 16 + SPAWN_STACK_SHARED * 4 * len(it.loads) * 128
@@ -1742,10 +1787,16 @@ class Lowered:
         """compile one of this item's programs with the call's options (cuda_math, min_blocks_per_sm)"""
         return compile_kernel(self.head + src, note, nbuf, smem, self.flags)
 
+    def _no_wider(self, what):
+        if self.it.acc:
+            raise NotImplementedError(f"tallymap_b200: {what} of an item with float64, int64 or scaled fixed-point "
+                                      "Sum outputs is not lowered (grad is)")
+
     def jvp_program(self, wrt, lanes):
         """the forward-mode program: the forward's outputs and, per tangent lane, the tangents of its float tallies
         for tangents of bc[wrt] given per launch (an input f32[lanes, len(wrt)])"""
         self._differentiable(wrt)
+        self._no_wider("forward mode")
         from .backend import ItemProgram, TSpec, Operand
         key = (tuple(wrt), int(lanes))
         if key not in self.jvps:
@@ -1783,10 +1834,12 @@ class Lowered:
         """the one-pass value-and-grad program for bc[wrt] (forward outputs, then the exact cotangent tally): with no
         active carry the step VJPs summed as the forward runs (OnePassVG); otherwise, for up to FWD_GRAD_MAX
         operands and no fixed-point output, forward mode with the tangents contracted at each emit
-        (jvp_source(contract=True)); else None (the replay)"""
+        (jvp_source(contract=True)); else None (the replay; also for an item with a wider accumulator)"""
         self._differentiable(wrt)
         from .backend import ItemProgram, TSpec, Operand
         wrt = tuple(wrt)
+        if self.it.acc:
+            return None
         if wrt not in self.vgs:
             prog = None
             sp = self.it.spawns
@@ -1848,6 +1901,7 @@ class Lowered:
         with each Records output's counts and offsets after the per-item operands; tangent fields "field#d<lane>"
         beside the fields, every capacity the placeholder 0"""
         self._differentiable(wrt)
+        self._no_wider("forward mode")
         from .backend import ItemProgram, TSpec, Operand
         key = ("fill", tuple(wrt), int(lanes))
         if key not in self.jvps:

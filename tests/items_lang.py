@@ -603,3 +603,20 @@ def loop_records(t, x, key, a):
         return k + 1, x + 0.1, t.add("h", 0, a * y)
     k, x, t = tl.while_loop(lambda c: c[0] < 4, body, (0, x, t))
     return t, k
+
+
+def accumulators(t, x, key, a):
+    """the wider accumulators (tallymap.Sum of float64, int64, and fixed_point with a scale): per step a drawn bin
+    b of 4 takes a float v = 1000 a (u - 0.5) into a float64 Sum and a scaled float64 one, 1 + k into an int64 Sum,
+    an int in [-50, 50) into a scaled int32 one, and the positive 500 a u into a float64 Sum at scale 2^50, whose
+    words carry past 2^63 many times"""
+    def body(c):
+        k, x, t = c
+        u = tl.random.uniform(tl.random.fold_in(key, k))
+        b = (u * 4).astype(tl.int32)
+        v = a * (u - 0.5) * 1000.0
+        t = t.add("f64", b, v).add("i64", b, 1 + k).add("w64", b, v)
+        t = t.add("wi32", b, (u * 100).astype(tl.int32) - 50).add("wbig", b, a * u * 500.0)
+        return k + 1, x + 0.05 * (2 * u - 1), t
+    k, x, t = tl.while_loop(lambda c: (c[1] >= 0) & (c[1] <= 1) & (c[0] < 100), body, (0, x, t))
+    return t, k

@@ -80,8 +80,13 @@ def test_fixed_point_sum_lowers_to_exact_bins():
     L = f.lowered(_args_walk())
     assert [t.exact for t in L.fwd.tallies] == [True, False]
     assert "ExactSum<256>::emit(c.sx0" in L.fwd_source and "ExactSum<256>::readout" in L.fwd_source
-    with pytest.raises(NotImplementedError):
-        tm.Sum((4,), tm.api.torch.int32, fixed_point=True)
+    # (another dtype with fixed_point: the scaled fixed-point sum; a dtype beyond float32 / int32 / float64 / int64
+    # and a scale that is not a positive finite number are refused)
+    assert tm.Sum((4,), tm.api.torch.int32, fixed_point=True).accumulator() == ("wide", tm.api.torch.int32, 2.0 ** 32)
+    with pytest.raises(TypeError):
+        tm.Sum((4,), tm.api.torch.float16)
+    with pytest.raises(ValueError):
+        tm.Sum((4,), tm.api.torch.float64, fixed_point=True, scale=0.0)
 
 
 def test_jvp_programs_compile():
@@ -696,7 +701,7 @@ def test_outputs_shorthand():
     """a bare shape in outputs is Sum(shape) (_api.py:509); Sum takes an int shape"""
     from items_lang import walk
     f = tm.vmap(walk, outputs={"hist": (256,), "side": tm.Sum(2)}, in_axes=(0, 0, None))
-    assert f.outputs == {"hist": ((256,), "f32", False), "side": ((2,), "f32", False)}
+    assert f.outputs == {"hist": ((256,), "f32", False, None), "side": ((2,), "f32", False, None)}
     assert tm.Sum(4).shape == (4,) and tm.Sum(()).shape == ()
 
 
@@ -1072,3 +1077,39 @@ def test_inner_while_loops():
         assert La.fwd.kernel > 0 and La.grad_program((0,)).kernel > 0 and La.jvp_program((0,), 2).kernel > 0
         assert La.vg_program((0,)).kernel > 0
         assert "for (int gw" in lower.grad_source(La.it, [0])[0]
+
+
+def _acc_outputs():
+    import torch
+    return {"f64": tm.Sum((4,), torch.float64), "i64": tm.Sum((4,), torch.int64),
+            "w64": tm.Sum((4,), torch.float64, fixed_point=True, scale=2.0 ** 20),
+            "wi32": tm.Sum((4,), torch.int32, fixed_point=True, scale=1.0),
+            "wbig": tm.Sum((4,), torch.float64, fixed_point=True, scale=2.0 ** 50)}
+
+
+def test_wider_accumulators_lower_and_evaluate():
+    """Sum outputs of float64 and int64 and scaled fixed-point Sums (tallymap/_api.py:55-84) lower to float64 /
+    int64 atomics and to the carry-word accumulator read out by the launch's last block; grad compiles (their
+    cotangents enter the float32 adjoint), value_and_grad falls back to it, forward mode refuses them; the IR
+    evaluator's scaled sums are exact integers (wbig: totals far past 2^63)"""
+    import torch
+    from oracle.ir_eval import Evaluator
+    from items_lang import accumulators
+    outs = _acc_outputs()
+    f = tm.vmap(accumulators, outputs=outs, in_axes=(0, 0, None), max_steps=200)
+    x0 = np.random.default_rng(1).uniform(0.3, 0.7, 64).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(2), 64)
+    L = f.lowered((x0, keys, np.float32(1.5)))
+    assert [t.dtype for t in L.fwd.tallies] == [torch.float64, torch.int64, torch.float64, torch.int32, torch.float64]
+    assert [t.wide for t in L.fwd.tallies] == [0.0, 0.0, 2.0 ** 20, 1.0, 2.0 ** 50]
+    assert "WideSum::readout" in L.fwd_source and "(unsigned long long*)&c.g1" in L.fwd_source
+    assert L.grad_program((0,)).kernel > 0 and L.vg_program((0,)) is None
+    with pytest.raises(NotImplementedError, match="forward mode"):
+        L.jvp_program((0,), 1)
+    wide = {"w64": ("f64", 2.0 ** 20), "wi32": ("i32", 1.0), "wbig": ("f64", 2.0 ** 50)}
+    specs = {k: ((4,), "f32" if k in ("f64", "w64", "wbig") else "i32") for k in outs}
+    tr = T.trace_item(accumulators, ["f32", "key", "f32"], 2, specs)
+    r = Evaluator(tr, 200, wide=wide).run([x0, keys], [np.float32(1.5)])
+    assert r["sums"]["i64"].dtype == np.int64 and r["sums"]["wi32"].dtype == np.int64
+    assert r["sums"]["wbig"].min() > 2.0 ** 63 / 2.0 ** 50 and not r["stats"][3]
+    assert np.abs(r["sums"]["w64"] - r["sums"]["f64"]).max() <= 64 * 100 * 2.0 ** -21

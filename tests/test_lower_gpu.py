@@ -1071,3 +1071,37 @@ def test_inner_while_loops_differentiated(cuda, name):
             x = f32(x + f32(0.1))
     want = float(ct[0]) * m_all
     assert abs(g - want) <= 1e-5 * abs(want), (g, want)
+
+
+def test_wider_accumulators(cuda):
+    """float64 and int64 Sums and scaled fixed-point Sums (tallymap/_api.py:55-84): the int64 and every scaled sum
+    bitwise the IR evaluator's exact integers (wbig's words carry past 2^63 many times: the 128-bit readout), the
+    float64 sum within 1e-12; the gradient w.r.t. a of the float outputs (linear in a) within 1e-5 of total / a"""
+    from items_lang import accumulators
+    from oracle.ir_eval import Evaluator
+    from tallymap_b200 import trace as Tr
+    from test_lower_cpu import _acc_outputs
+    n = 1500
+    x0 = np.random.default_rng(1).uniform(0.3, 0.7, n).astype(np.float32)
+    keys = prng.split(prng.PRNGKey(2), n)
+    a = np.float32(1.5)
+    outs = _acc_outputs()
+    wide = {"w64": ("f64", 2.0 ** 20), "wi32": ("i32", 1.0), "wbig": ("f64", 2.0 ** 50)}
+    specs = {k: ((4,), "f32" if k in ("f64", "w64", "wbig") else "i32") for k in outs}
+    ref = Evaluator(Tr.trace_item(accumulators, ["f32", "key", "f32"], 2, specs), 200, wide=wide).run([x0, keys], [a])
+    f = tm.vmap(accumulators, outputs=outs, in_axes=(0, 0, None), max_steps=200)
+    r = f(x0, keys, a)
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in r.outputs.items()}
+    assert got["i64"].dtype == np.int64 and np.array_equal(got["i64"], ref["sums"]["i64"])
+    assert got["wi32"].dtype == np.int32 and np.array_equal(got["wi32"], ref["sums"]["wi32"])
+    for k in ("w64", "wbig"):
+        assert got[k].dtype == np.float64 and np.array_equal(got[k].view(np.uint64), ref["sums"][k].view(np.uint64)), k
+    assert np.abs(got["f64"] - ref["sums"]["f64"]).max() <= 1e-12 * np.abs(ref["sums"]["f64"]).max()
+    assert int(r.stats["fixed_point_overflow"]) == 0 and np.array_equal(r.per_item.cpu().numpy(), ref["results"][0])
+    ct = {"f64": torch.tensor([0.5, -1.0, 2.0, 0.25], dtype=torch.float64), "wbig": torch.tensor([1.0, 0.0, 0.0, -1.0])}
+    g = float(f.grad(x0, keys, a, wrt=2, cotangents=ct))
+    _, gv = f.value_and_grad(x0, keys, a, wrt=2, cotangents=ct)
+    want = (float(np.dot(ct["f64"].numpy(), ref["sums"]["f64"])) +
+            float(np.dot(ct["wbig"].double().numpy(), ref["sums"]["wbig"]))) / float(a)
+    assert abs(g - want) <= 1e-5 * abs(want) and float(gv) == g
