@@ -40,12 +40,12 @@ def contiguous_span(group):
 
 
 def all_reduce_sums(tensors):
-    """in place: all_reduce(SUM) of float32 and int32 tensors, one collective per dtype.  Tensors of a dtype that
+    """in place: all_reduce(SUM) of float32, int32, float64 and int64 tensors, one collective per dtype.  Tensors of a dtype that
     are one contiguous range (a single tensor, or tallies laid out back to back by backend.alloc_results) are
     reduced in place; otherwise they are packed into a flat buffer and copied back."""
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return tensors
-    for dt in (torch.float32, torch.int32):
+    for dt in (torch.float32, torch.int32, torch.float64, torch.int64):
         group = [t for t in tensors if t.dtype == dt]
         if not group:
             continue
@@ -85,4 +85,38 @@ def combine_exact(words, n_bins, out, stats):
     st = torch.cuda.current_stream(words.device).cuda_stream
     _lib.check(_lib.lib().tm_exact_combine(ctypes.c_void_p(st), ctypes.c_void_p(gathered.data_ptr()), world, n_bins,
                                            ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stats.data_ptr())))
+    return out
+
+
+def combine_wide(words, out, scale, stats=None):
+    """the cross-rank total of a scaled fixed-point Sum (Sum(fixed_point=True) of float64 / int32 / int64): every
+    rank's words all_gathered (per bin an int64 low word, then the i32 carries and u32 flags: 16 bytes per bin), each
+    bin's exact integer total -- lo + carry * 2^64 summed over the ranks -- formed in Python integers, and read out
+    once into `out` as the single-GPU launch reads out its own: the correctly rounded double of the total (Python's
+    int -> float) times 1 / scale, NaN for a flagged float bin, the conversion toward zero saturating for an integer
+    one; a value out of the output's range counts in stats[3].  Bitwise the single-GPU result, whatever the number of
+    ranks (the words of an order-independent integer sum)."""
+    S = out.numel()
+    g = gather_words(words).cpu()
+    lo = g[:, :S].numpy()
+    cf = g[:, S:].contiguous().view(torch.int32).numpy()
+    carry, flag = cf[:, :S], cf[:, S:]
+    inv = 1.0 / float(scale)
+    vals, over = [], 0
+    floating = out.dtype == torch.float64
+    lim = 2 ** 63 if out.dtype == torch.int64 else 2 ** 31
+    for b in range(S):
+        tot = sum(int(lo[r, b]) + (int(carry[r, b]) << 64) for r in range(g.shape[0]))
+        bad = bool(flag[:, b].any())
+        v = float(tot) * inv
+        if floating:
+            big = not abs(v) <= 1.7976931348623157e308
+            over += int(big and not bad)
+            vals.append(float("nan") if bad or big else v)
+        else:
+            over += int(not -lim <= v < lim)
+            vals.append(lim - 1 if v >= lim else -lim if v < -lim else int(v))
+    out.copy_(torch.tensor(vals, dtype=out.dtype))
+    if stats is not None and over:
+        stats[3] += over
     return out

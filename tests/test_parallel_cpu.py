@@ -90,6 +90,19 @@ def _worker(rank, world, port, mode, q):
             w = torch.from_numpy(words_of(orc, vals[part], bins[part], nb))
             g = parallel.gather_words(w)
             q.put((rank, combine_host(g.numpy(), nb).view(np.uint32).tolist()))
+        elif mode == "wide":
+            # scaled fixed-point words (lo, then carry and flag int32 pairs) whose totals need the carries: rank r's
+            # bin 0 holds 2^63 - 1 + r wrapped (carry 1 on rank 1), bin 1 -2^62 per rank, bin 2 a flag on rank 1
+            S = 3
+            lo = torch.tensor([2 ** 63 - 1 if rank == 0 else -(2 ** 63), -(2 ** 62), 5], dtype=torch.int64)
+            cf = torch.tensor([0 if rank == 0 else 1, 0, 0, 0, 0, rank], dtype=torch.int32)
+            w = torch.cat([lo, cf.view(torch.int64)])
+            out = torch.zeros(S, dtype=torch.float64)
+            st = torch.zeros(5, dtype=torch.int32)
+            parallel.combine_wide(w, out, 2.0 ** 4, st)
+            out_i = torch.zeros(S, dtype=torch.int64)
+            parallel.combine_wide(w, out_i, 1.0, st)
+            q.put((rank, out.tolist(), out_i.tolist(), st.tolist()))
         elif mode == "fail":
             if rank == 1:
                 raise SystemExit(3)                    # this rank dies before the collective
@@ -148,3 +161,15 @@ def test_rank_failure_is_detected_not_hung():
     res, codes = run2("fail")
     assert codes[1] == 3
     assert res and res[0][0] == 0 and res[0][1] != "no error"
+
+
+def test_wide_words_combine_two_ranks():
+    """scaled fixed-point Sums across ranks: the exact integer total of the ranks' (low word, carry) pairs read out
+    once -- bin 0's total (2^63 - 1) + (-2^63 + 2^64) = 2^64 - 1 needs rank 1's carry; a flag on either rank makes a
+    float bin NaN; an int64 output of a total past 2^63 saturates and counts in stats[3]"""
+    import math
+    res, codes = run2("wide")
+    assert codes == [0, 0] and len(res) == 2
+    for _, f64, i64, st in res:
+        assert f64[0] == float(2 ** 64 - 1) / 16.0 and f64[1] == -(2.0 ** 63) / 16.0 and math.isnan(f64[2])
+        assert i64 == [2 ** 63 - 1, -(2 ** 63), 10] and st[3] == 1
