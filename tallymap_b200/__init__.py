@@ -13,7 +13,16 @@ from . import lang, prng
 from ._lib import TallymapError, build
 from .api import FAMILIES, Queue, Records, Result, Sum, TallyError, UnsupportedError, vmap
 from .backend import PROGRAMS, STATS, ItemProgram, TSpec, run
+from .memory import OutputMemory, call_memory, cell_bytes, max_cells, output_memory
 
 __version__ = "0.1.0"
-__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "Queue", "Records", "Result", "Sum", "TSpec", "TallyError",
-           "TallymapError", "UnsupportedError", "build", "lang", "prng", "run", "vmap"]
+__all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "OutputMemory", "Queue", "Records", "Result", "Sum", "TSpec",
+           "TallyError", "TallymapError", "UnsupportedError", "build", "call_memory", "cell_bytes", "lang",
+           "max_cells", "output_memory", "prng", "run", "supported_primitives", "vmap"]
+
+
+def supported_primitives():
+    """the jaxpr primitives the jaxpr front end lowers (tallymap.supported_primitives): the sorted names of
+    tallymap_b200.from_jaxpr's table"""
+    from . import from_jaxpr
+    return from_jaxpr.supported_primitives()

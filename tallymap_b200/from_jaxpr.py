@@ -780,6 +780,22 @@ def _platform_index(platforms):
                                "default")
 
 
+_STRUCTURAL = ("pjit", "jit", "closed_call", "core_call", "remat", "remat2", "checkpoint", "custom_jvp_call",
+               "custom_vjp_call", "custom_vjp_call_jaxpr", "while", "cond", "scan", "tallymap_emit", "tallymap_claim",
+               "tallymap_spawn", "threefry2x32", "reshape", "squeeze", "expand_dims", "copy", "copy_p",
+               "optimization_barrier", "broadcast_in_dim", "convert_element_type", "bitcast_convert_type",
+               "reduce_precision", "iota", "slice", "gather", "dynamic_slice", "dynamic_update_slice", "concatenate",
+               "reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "argmax", "argmin", "sort", "rev",
+               "transpose", "pad", "dot_general", "iota_2x32_shape", "platform_index", "select_n", "clamp",
+               "integer_pow", "round", "div", "rem", "pow", "atan2", "nextafter", "shift_left",
+               "shift_right_logical", "shift_right_arithmetic")
+
+
+def supported_primitives():
+    """the names of the jaxpr primitives this front end lowers, sorted (tallymap.supported_primitives)"""
+    return sorted(set(_STRUCTURAL) | set(_CUM) | set(_UNARY) | set(_FOLD2) | set(_RANDOM))
+
+
 def _vec(f, x):
     return T.Vec(f(v) for v in x) if isinstance(x, T.Vec) else f(x)
 

@@ -1113,3 +1113,30 @@ def test_wider_accumulators_lower_and_evaluate():
     assert r["sums"]["i64"].dtype == np.int64 and r["sums"]["wi32"].dtype == np.int64
     assert r["sums"]["wbig"].min() > 2.0 ** 63 / 2.0 ** 50 and not r["stats"][3]
     assert np.abs(r["sums"]["w64"] - r["sums"]["f64"]).max() <= 64 * 100 * 2.0 ** -21
+
+
+def test_memory_model_matches_the_layout():
+    """tallymap_b200.output_memory / cell_bytes / call_memory / max_cells (tallymap/_memory.py:155-260): the per-cell
+    bytes of each Sum kind equal what the forward program's result layout allocates for that output (the output and
+    its accumulator words); derivatives add the tangent tallies or the cotangent; supported_primitives lists the jaxpr
+    front end's table"""
+    from items_lang import accumulators
+    outs = dict(_acc_outputs(), f64=tm.Sum((4,), tm.api.torch.float64))
+    f = tm.vmap(accumulators, outputs=outs, in_axes=(0, 0, None), max_steps=200)
+    x0 = np.float32([0.5, 0.4])
+    L = f.lowered((x0, prng.split(prng.PRNGKey(2), 2), np.float32(1.5)))
+    layout, _ = L.fwd.result_layout(2)
+    for nm, o in outs.items():
+        allocated = sum(nb for name, nb, _, _ in layout if name == nm or name.startswith(nm + "."))
+        assert tm.output_memory(o).per_cell * 4 == allocated, nm
+    ex = tm.Sum((1000,), fixed_point=True)
+    assert tm.output_memory(ex).per_cell == 48 and tm.output_memory(ex, "jvp", lanes=2).per_cell == 48 + 2 * 48
+    assert tm.output_memory(tm.Sum(8), "grad").per_cell == 4 and tm.output_memory(tm.Sum(8), "vjp").per_cell == 8
+    assert tm.cell_bytes(ex, cells=10) == (48 * 10 + tm.memory._LAUNCH) / 10
+    assert tm.call_memory({"a": tm.Sum((4,)), "b": ex}) == 4 * 4 + 48 * 1000 + tm.memory._LAUNCH
+    assert tm.max_cells(tm.Sum(1)) == 2 ** 31 - 1 and tm.max_cells(ex, memory=48 * 100 + tm.memory._LAUNCH) == 100
+    with pytest.raises(ValueError):
+        tm.output_memory(tm.Sum(4, tm.api.torch.float64), "jvp")
+    prims = tm.supported_primitives()
+    assert {"while", "cond", "scan", "tallymap_emit", "tallymap_claim", "gather", "sort", "exp"} <= set(prims)
+    assert "fft" not in prims and prims == sorted(prims)
