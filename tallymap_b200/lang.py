@@ -8,7 +8,9 @@ erfinv primitives (random.normal over erfinv as jax.random forms it, random.expo
 randint), ceil, log10, logistic, isfinite and the other jax.numpy compositions below; small vectors with jax.numpy's
 elementwise semantics (trace.Vec: array, stack, dot, reductions, a traced index read as jnp does); broadcast tables
 read by traced indices (trace.Table); cond / switch (both branches traced, results selected, a branch's t.add /
-t.append / t.spawn made only where it is taken) and fori_loop / scan of static lengths.
+t.append / t.spawn made only where it is taken, an inner loop in a branch iterating only where it is taken);
+while_loop -- the item's first top-level one is its stepping loop, any other an inner loop --; fori_loop (static
+bounds: unrolled; a traced bound: an inner loop) and scan of a static length.
 
     from tallymap_b200 import lang as tl
 
