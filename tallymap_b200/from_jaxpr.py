@@ -28,9 +28,10 @@ the taken branch), scan of a static length (unrolled; jax's static fori_loop), p
 operations on scalars and small vectors (reshape, broadcast_in_dim, squeeze, expand_dims, slice, dynamic_slice,
 dynamic_update_slice, concatenate, pad, rev, iota, reductions, cumsum / cumprod / cummax / cummin, dot_general with
 a result of at most one dimension, sort on one key, gather as jnp indexing writes it -- a broadcast array of two
-dimensions or above 64 elements is a table read by index --), jit (jax >= 0.7's name for pjit), random_clone /
-random_key_data, iota_2x32_shape and platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a
-primitive its table lacks (backends/kernel/__init__.py:81-82): never a fallback.
+dimensions or above 64 elements is a table read by index --, element scatters into a vector: x.at[i].set / add /
+multiply / min / max), jit (jax >= 0.7's name for pjit), random_clone / random_key_data, iota_2x32_shape and
+platform_index.  Anything else raises UnsupportedError, as the reference's emitter does for a primitive its table
+lacks (backends/kernel/__init__.py:81-82): never a fallback.
 
 `run(p, pi, bc, target, cuda_math, schedule, ndev, min_blocks_per_sm)` is the reference's backend entry
 (tallymap/backends/kernel/__init__.py:135-185) over a reference ItemProgram: its jaxpr through this front end,
@@ -327,6 +328,8 @@ class _Interp:
             return [T.Vec(tuple.__getitem__(x, i) for i in range(s0, s1, st))]
         if p == "gather":
             return [_gather(e, a[0], a[1], prm)]
+        if p in _SCATTER:
+            return [_scatter(p, e, a[0], a[1], a[2], prm)]
         if p == "dynamic_slice" and isinstance(a[0], T.Table) and len(a[0].shape) == 2:
             return [_table_slice(a[0], [_py(v) for v in a[1:3]], [int(d) for d in prm["slice_sizes"]])]
         if p == "dynamic_slice":
@@ -716,6 +719,46 @@ def _clamp_start(i, hi):
     return tl.clip(i, 0, hi)
 
 
+_SCATTER = {"scatter": (None, lambda o, u: u), "scatter-add": (np.add, lambda o, u: o + u),
+            "scatter_add": (np.add, lambda o, u: o + u), "scatter-mul": (np.multiply, lambda o, u: o * u),
+            "scatter_mul": (np.multiply, lambda o, u: o * u), "scatter-min": (np.minimum, tl.minimum),
+            "scatter_min": (np.minimum, tl.minimum), "scatter-max": (np.maximum, tl.maximum),
+            "scatter_max": (np.maximum, tl.maximum)}
+
+
+def _scatter(p, e, x, idx, upd, prm):
+    """lax.scatter / scatter-add / -mul / -min / -max into a vector, as x.at[i].set / add / multiply / min / max
+    write it: each update (the updates in order, one element per index vector of the indices' last axis) combined
+    into the element its index names; an out-of-range index drops its update (mode fill_or_drop, jax's default for
+    scatters) or is clamped (clip, promise_in_bounds); a traced index selects per element"""
+    dn = prm["dimension_numbers"]
+    oshape = tuple(e.invars[0].aval.shape)
+    if len(oshape) != 1 or tuple(getattr(dn, "operand_batching_dims", ()) or ()):
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a scatter into anything but a vector")
+    if tuple(dn.update_window_dims) or tuple(dn.inserted_window_dims) != (0,):
+        raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: a scatter of windows (element scatters only)")
+    n = oshape[0]
+    clip = _mode(prm.get("mode")) == "clip" and "FILL" not in str(prm.get("mode")).upper()
+    f_np, f_tl = _SCATTER[p]
+    xs = list(x) if isinstance(x, T.Vec) else [x]
+    ivals = list(idx) if isinstance(idx, T.Vec) else [idx]
+    uvals = list(upd) if isinstance(upd, T.Vec) else [upd] * len(ivals)
+    for i, u in zip(ivals, uvals):
+        i = _py(i)
+        if isinstance(i, int):
+            if not 0 <= i < n:
+                if not clip:
+                    continue
+                i = int(np.clip(i, 0, n - 1))
+            xs[i] = u if f_np is None else _arith(f_np, f_tl, xs[i], u)
+            continue
+        i = tl.clip(i, 0, n - 1) if clip else i
+        for j in range(n):
+            new_j = u if f_np is None else _arith(f_np, f_tl, xs[j], u)
+            xs[j] = tl.where(i == j, _py(new_j), _py(xs[j]))
+    return T.Vec(xs)
+
+
 def _gather(e, x, idx, prm):
     """lax.gather in the forms jnp indexing writes for 1-D and 2-D operands: each index vector (the last axis of
     the indices) starts a slice of `slice_sizes`, the collapsed dimensions dropped, the rest kept; the result at
@@ -786,7 +829,9 @@ _STRUCTURAL = ("pjit", "jit", "closed_call", "core_call", "remat", "remat2", "ch
                "optimization_barrier", "broadcast_in_dim", "convert_element_type", "bitcast_convert_type",
                "reduce_precision", "iota", "slice", "gather", "dynamic_slice", "dynamic_update_slice", "concatenate",
                "reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "argmax", "argmin", "sort", "rev",
-               "transpose", "pad", "dot_general", "iota_2x32_shape", "platform_index", "select_n", "clamp",
+               "transpose", "pad", "dot_general", "iota_2x32_shape", "platform_index", "select_n", "clamp", "scatter",
+               "scatter-add", "scatter_add", "scatter-mul", "scatter_mul", "scatter-min", "scatter_min",
+               "scatter-max", "scatter_max",
                "integer_pow", "round", "div", "rem", "pow", "atan2", "nextafter", "shift_left",
                "shift_right_logical", "shift_right_arithmetic")
 

@@ -369,6 +369,57 @@ def test_inner_while_in_a_jaxpr():
     assert np.array_equal(np.asarray(r["results"][1]).view(np.uint32), np.asarray(rq["results"][1]).view(np.uint32))
 
 
+def test_scatter_primitives():
+    """x.at[i].set / add / multiply / max into a vector (lax.scatter and its combining forms): static and traced
+    indices, an out-of-range index dropped (fill_or_drop, jax's default) or clamped (clip); the IR evaluator's values
+    equal numpy's in update order"""
+    from types import SimpleNamespace as NS
+    from oracle.ir_eval import Evaluator
+    V, E, L = J.Var, J.Eqn, J.Literal
+    dn = NS(update_window_dims=(), inserted_window_dims=(0,), scatter_dims_to_operand_dims=(0,),
+            operand_batching_dims=(), scatter_indices_batching_dims=())
+    DROP, CLIP = "GatherScatterMode.FILL_OR_DROP", "GatherScatterMode.CLIP"
+    x, y, i = V(J.F, (4,)), V(J.F), V(J.I)
+    ib, s1, s2, s3, s4, s5 = V(J.I, (1,)), V(J.F, (4,)), V(J.F, (4,)), V(J.F, (4,)), V(J.F, (4,)), V(J.F, (4,))
+    sc = lambda p_, ins, out, mode: E(p_, ins, [out], dimension_numbers=dn, indices_are_sorted=True,
+                                      unique_indices=True, mode=mode, update_jaxpr=None, update_consts=())
+    eqns = [E("broadcast_in_dim", [i], [ib], shape=(1,), broadcast_dimensions=()),
+            sc("scatter", [x, ib, y], s1, DROP),
+            sc("scatter-add", [x, ib, y], s2, CLIP),
+            sc("scatter-mul", [x, L(np.array([2], np.int32), J.I), y], s3, DROP),
+            sc("scatter-max", [x, ib, y], s4, DROP),
+            sc("scatter-add", [x, L(np.array([7], np.int32), J.I), y], s5, DROP)]
+    cj = J.ClosedJaxpr(J.Jaxpr([x, y, i], [s1, s2, s3, s4, s5], eqns))
+    fn, specs = FJ.item_function(cj, [], 3)
+    tr = T.trace_item(fn, specs, 3, {})
+    n = 30
+    rng = np.random.default_rng(3)
+    xs = rng.normal(size=(n, 4)).astype(np.float32)
+    ys = rng.normal(size=n).astype(np.float32)
+    ii = rng.integers(-2, 6, n).astype(np.int32)
+    res = [np.asarray(r) for r in Evaluator(tr, 1).run([xs, ys, ii], [])["results"]]
+    for q in range(n):
+        x0, v, k = xs[q], ys[q], int(ii[q])
+        want = []
+        a = x0.copy()
+        if 0 <= k < 4:
+            a[k] = v
+        want.append(a)
+        a = x0.copy()
+        a[int(np.clip(k, 0, 3))] += v
+        want.append(a)
+        a = x0.copy()
+        a[2] *= v
+        want.append(a)
+        a = x0.copy()
+        if 0 <= k < 4:
+            a[k] = np.maximum(a[k], v)
+        want.append(a)
+        want.append(x0.copy())
+        got = np.float32([res[j][q] for j in range(20)]).reshape(5, 4)
+        assert np.array_equal(got, np.float32(want)), q
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
