@@ -669,10 +669,10 @@ def tree_adjoint(adj, t, cts, max_steps=100000, rev_checkpoints=None, stream=Non
     bad = (tree[0] > 0) | (tree[1] > 0) | (fstats[STATS.index("children_truncated")] > 0) | \
         (fstats[STATS.index("children_dropped")] > 0) | outs[-2].bool().any() | bool(t["incomplete"])
     tree_adjoint.last = dict(ctl=outs[0], fwd_ctl=t["ctl"])
-    return dict(g=g_out, ct_in=outs[5:5 + len(adj.ys) - 1], poisoned=bad, words=outs[2], stats=outs[3],
-                info=dict(children=t["total"], generations=t["G"], launches=launches + 2, kernels=launches + 4,
-                          record=t["R"], poisoned=bad, mismatch=tree[0], replay_truncated=tree[1],
-                          generation_sizes=cnt[:t["G"] + 1].tolist()))
+    info = dict(children=t["total"], generations=t["G"], launches=launches + 2, kernels=launches + 4, record=t["R"],
+                poisoned=bad, mismatch=tree[0], replay_truncated=tree[1], generation_sizes=cnt[:t["G"] + 1].tolist())
+    tree_adjoint.last_info = info
+    return dict(g=g_out, ct_in=outs[5:5 + len(adj.ys) - 1], poisoned=bad, words=outs[2], stats=outs[3], info=info)
 
 
 def tree_grad(pi, X0, ct_dep, max_steps=100000, queue=None, record=None, rev_checkpoints=None, stream=None):

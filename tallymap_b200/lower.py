@@ -18,6 +18,7 @@ import ctypes
 import dataclasses
 import hashlib
 import os
+import time
 
 import numpy as np
 import torch
@@ -972,12 +973,15 @@ def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
         return kid
     L = _lib.lib()
     d = cache_dir()
+    t0 = time.perf_counter()
     path = os.path.join(d, hashlib.sha256((digest + _headers_digest()).encode()).hexdigest() + ".cubin") if d else None
     image = None
+    compiled_here = False
     if path and os.path.exists(path):
         with open(path, "rb") as fh:
             image = fh.read()
     if image is None:
+        compiled_here = True
         n = ctypes.c_size_t()
         _lib.check(L.tm_compile(source.encode(), CSRC.encode(), 128, flags, None, 0, ctypes.byref(n)))
         buf = ctypes.create_string_buffer(n.value)
@@ -994,6 +998,10 @@ def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
                 pass                           # (a read-only home: no disk cache)
     _lib.check(L.tm_register(ctypes.c_int64(kid), image, len(image), note.encode(), n_buffers, smem_bytes, 128))
     _COMPILED[kid] = note
+    from . import _diagnostics as diagnostics
+    diagnostics.record_kernel(dict(tag=note, kernel=kid, source_sha256=digest, buffers=n_buffers,
+                                   shared_bytes=smem_bytes, compile_s=round(time.perf_counter() - t0, 3),
+                                   from_disk_cache=not compiled_here))
     from . import backend
     backend.COMPILED[kid] = n_buffers
     return kid
@@ -1741,6 +1749,15 @@ class Lowered:
         acc = {k: v[3] for k, v in outputs.items() if len(v) > 3 and v[3]}
         self.tr = T.trace_item(fn, in_specs, n_per_item, specs, recs, spawn=spawn)
         self.it = Item(self.tr, in_specs, self.name, exact, acc)
+        from . import _diagnostics as diagnostics
+        tr = self.tr
+        floats = sorted({float(x.value) for e in T._walk(tr.pre + tr.cond + tr.body + tr.post) for x in e.ins
+                         if isinstance(x, T.Lit) and x.dtype == T.F32})
+        diagnostics.record_program(dict(tag=self.name, inputs=list(in_specs), n_per_item=n_per_item,
+                                        outputs={k: v[0] for k, v in outputs.items()}, records=sorted(recs),
+                                        equations=dict(pre=len(tr.pre), cond=len(tr.cond), body=len(tr.body),
+                                                       post=len(tr.post)),
+                                        float_literals=floats[:32]))
         it = self.it
         src, smem = forward_source(it)
         self.fwd_source = src

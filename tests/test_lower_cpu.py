@@ -1140,3 +1140,19 @@ def test_memory_model_matches_the_layout():
     prims = tm.supported_primitives()
     assert {"while", "cond", "scan", "tallymap_emit", "tallymap_claim", "gather", "sort", "exp"} <= set(prims)
     assert "fft" not in prims and prims == sorted(prims)
+
+
+def test_diagnostics_and_history():
+    """tallymap_b200.diagnostics / history (tallymap/_diagnostics.py:1-53): the last lowered item programs (their
+    equation counts and the float literals they closed over) and compiled kernels (tag, id, source digest, compile
+    time or the disk cache), the environment and the device; reset clears the history"""
+    tm.diagnostics(reset=True)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    f.lowered(_args_walk())
+    h = tm.history()
+    assert h["programs"][-1]["tag"] == "walk" and h["programs"][-1]["equations"]["body"] > 0
+    assert 0.02 in h["programs"][-1]["float_literals"]
+    assert any(k["tag"] == "walk_fwd" and len(k["source_sha256"]) == 64 for k in h["kernels"])
+    d = tm.diagnostics(reset=True)
+    assert d["versions"]["tallymap_b200"] and d["cuda"]["arch"] == "sm_100a" and "cuda_available" in d["platform"]
+    assert d["programs"] and not tm.history()["programs"]
