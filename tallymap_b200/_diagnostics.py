@@ -8,7 +8,7 @@ counterpart of tallymap.diagnostics / history, tallymap/_diagnostics.py:1-53, fo
     tm.diagnostics(reset=True)    the same, then the history cleared
     tm.history()                  cheap: the last item programs and kernel records, nothing probed
 
-Kernel records come from lower.compile_kernel (tag, kernel id, source digest, compile seconds or "disk cache"),
+Kernel records come from lower.compile_kernel (tag, kernel id, source digest, compile seconds, the cache that held it),
 program records from lower.Lowered (item name, equations per part, input specs, outputs, the float constants the
 item closed over -- a derivative cannot reach them: what you differentiate must be an argument)."""
 import collections

@@ -969,7 +969,10 @@ def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
     tm_compile's (1: FMA contraction); a nonzero value enters the digest."""
     digest = hashlib.sha256(source.encode() + (b"" if not flags else f"/flags={flags}".encode())).hexdigest()
     kid = int(digest[:15], 16)          # a positive int64 id
+    from . import _diagnostics as diagnostics
     if kid in _COMPILED:
+        diagnostics.record_kernel(dict(tag=note, kernel=kid, source_sha256=digest, buffers=n_buffers,
+                                       shared_bytes=smem_bytes, compile_s=0.0, cache="process"))
         return kid
     L = _lib.lib()
     d = cache_dir()
@@ -998,10 +1001,9 @@ def compile_kernel(source, note, n_buffers, smem_bytes, flags=0):
                 pass                           # (a read-only home: no disk cache)
     _lib.check(L.tm_register(ctypes.c_int64(kid), image, len(image), note.encode(), n_buffers, smem_bytes, 128))
     _COMPILED[kid] = note
-    from . import _diagnostics as diagnostics
     diagnostics.record_kernel(dict(tag=note, kernel=kid, source_sha256=digest, buffers=n_buffers,
                                    shared_bytes=smem_bytes, compile_s=round(time.perf_counter() - t0, 3),
-                                   from_disk_cache=not compiled_here))
+                                   cache="none" if compiled_here else "disk"))
     from . import backend
     backend.COMPILED[kid] = n_buffers
     return kid
