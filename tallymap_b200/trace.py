@@ -303,6 +303,13 @@ class Vec(tuple):
     def shape(self):
         return (len(self),)
 
+    @property
+    def at(self):
+        """x.at[i].set(y) / add / multiply / min / max / get, jax.numpy's functional updates: a negative index counts
+        from the end; an update at an index still out of range is dropped (mode 'drop', jnp's default for updates)
+        or clamped (mode 'clip'); a traced index selects per element"""
+        return _VecAt(self)
+
     def _op(prim, out=None):
         return lambda self, o: _binary(prim, self, o, out)
 
@@ -350,6 +357,69 @@ class Vec(tuple):
         for j in range(1, n):
             r = lang.where(ii == j, tuple.__getitem__(self, j), r)
         return r
+
+
+class _VecAt:
+    __slots__ = ("v",)
+
+    def __init__(self, v):
+        self.v = v
+
+    def __getitem__(self, i):
+        return _VecRef(self.v, i)
+
+
+class _VecRef:
+    __slots__ = ("v", "i")
+
+    def __init__(self, v, i):
+        self.v, self.i = v, i
+
+    def get(self, mode=None):
+        if mode not in (None, "clip", "promise_in_bounds"):
+            raise UnsupportedError(f"tallymap_b200.lang: x.at[i].get(mode={mode!r})")
+        return self.v[self.i]
+
+    def _update(self, y, f, mode):
+        from . import lang
+        if mode not in (None, "drop", "fill", "clip", "promise_in_bounds"):
+            raise UnsupportedError(f"tallymap_b200.lang: x.at[i] update with mode={mode!r}")
+        clip = mode in ("clip", "promise_in_bounds")
+        xs, n, i = list(tuple.__iter__(self.v)), len(self.v), self.i
+        if isinstance(i, bool):
+            raise TraceError("tallymap_b200.lang: a vector index is an integer")
+        if isinstance(i, int):
+            i = i + n if i < 0 else i
+            if not 0 <= i < n:
+                if not clip:
+                    return Vec(xs)
+                i = min(max(i, 0), n - 1)
+            xs[i] = f(xs[i], y)
+            return Vec(xs)
+        i = _lit(i)
+        if not isinstance(i, Var) or i.dtype != I32:
+            raise TraceError("tallymap_b200.lang: a vector index is an int32")
+        ii = lang.where(i < 0, i + n, i)
+        if clip:
+            ii = lang.clip(ii, 0, n - 1)
+        return Vec(lang.where(ii == j, f(x, y), x) for j, x in enumerate(xs))
+
+    def set(self, y, mode=None):
+        return self._update(y, lambda x, y_: y_, mode)
+
+    def add(self, y, mode=None):
+        return self._update(y, lambda x, y_: x + y_, mode)
+
+    def multiply(self, y, mode=None):
+        return self._update(y, lambda x, y_: x * y_, mode)
+
+    def min(self, y, mode=None):
+        from . import lang
+        return self._update(y, lang.minimum, mode)
+
+    def max(self, y, mode=None):
+        from . import lang
+        return self._update(y, lang.maximum, mode)
 
 
 class Table:

@@ -1156,3 +1156,40 @@ def test_diagnostics_and_history():
     d = tm.diagnostics(reset=True)
     assert d["versions"]["tallymap_b200"] and d["cuda"]["arch"] == "sm_100a" and "cuda_available" in d["platform"]
     assert d["programs"] and not tm.history()["programs"]
+
+
+def test_vector_at_updates():
+    """x.at[i].set / add / multiply / min / max / get on a per-item vector, static and traced indices (negative
+    from the end; out of range dropped by default, clamped with mode='clip'): the IR evaluator against numpy"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, v, i, y):
+        a = v.at[i].set(y)
+        b = v.at[i].add(y, mode="clip")
+        c = v.at[-1].multiply(y)
+        d = v.at[i].max(y)
+        e = v.at[7].set(y)
+        return t, a, b, c, d, e, v.at[i].get()
+    tr = T.trace_item(item, [("f32", 4), "i32", "f32"], 3, {})
+    n = 40
+    rng = np.random.default_rng(5)
+    vs = rng.normal(size=(n, 4)).astype(np.float32)
+    ii = rng.integers(-6, 7, n).astype(np.int32)
+    ys = rng.normal(size=n).astype(np.float32)
+    res = [np.asarray(r) for r in Evaluator(tr, 1).run([vs, ii, ys], [])["results"]]
+    for q in range(n):
+        v, k, y = vs[q], int(ii[q]), ys[q]
+        kk = k + 4 if k < 0 else k
+        a = v.copy()
+        if 0 <= kk < 4:
+            a[kk] = y
+        b = v.copy()
+        b[min(max(kk, 0), 3)] += y
+        c = v.copy()
+        c[3] *= y
+        d = v.copy()
+        if 0 <= kk < 4:
+            d[kk] = max(d[kk], y)
+        want = np.concatenate([a, b, c, d, v, [v[min(max(kk, 0), 3)]]]).astype(np.float32)
+        got = np.float32([res[j][q] for j in range(21)])
+        assert np.array_equal(got, want), q
