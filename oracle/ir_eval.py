@@ -142,6 +142,10 @@ def _eval(e, a):
         return _wrap32(r) if d == T.I32 else r & 0xFFFFFFFF
     if p == "not":
         return (not a[0]) if d == T.BOOL else (_wrap32(~a[0]) if d == T.I32 else (~a[0]) & 0xFFFFFFFF)
+    if p == "popc":
+        return bin(int(a[0]) & 0xFFFFFFFF).count("1")
+    if p == "clz":
+        return 32 - (int(a[0]) & 0xFFFFFFFF).bit_length()
     if p == "shl":
         sh = a[1] & 0xFFFFFFFF
         return 0 if sh >= 32 else (_wrap32(a[0] << sh) if d == T.I32 else (a[0] << sh) & 0xFFFFFFFF)

@@ -217,9 +217,12 @@ _UNARY = {
     "erf": tl.erf, "erfc": tl.erfc, "erf_inv": tl.erfinv, "exp2": tl.exp2, "cbrt": tl.cbrt, "logistic": tl.logistic,
     "floor": tl.floor, "ceil": tl.ceil, "abs": tl.abs, "sign": tl.sign, "is_finite": tl.isfinite,
     "stop_gradient": tl.stop_gradient, "square": lambda x: x * x, "neg": lambda x: -x, "not": lambda x: ~x,
-    "rsqrt": lambda x: 1.0 / tl.sqrt(x),
+    "rsqrt": lambda x: 1.0 / tl.sqrt(x), "lgamma": tl.lgamma, "population_count": tl.population_count,
+    "clz": tl.clz,
 }
-_NP_UNARY = {"neg": np.negative, "abs": np.abs, "not": np.invert, "floor": np.floor, "ceil": np.ceil,
+_NP_UNARY = {"population_count": lambda v: bin(int(v) & 0xFFFFFFFF).count("1"),
+             "clz": lambda v: 32 - (int(v) & 0xFFFFFFFF).bit_length(),
+             "neg": np.negative, "abs": np.abs, "not": np.invert, "floor": np.floor, "ceil": np.ceil,
              "sign": np.sign, "exp": np.exp, "log": np.log, "sqrt": np.sqrt, "square": np.square}
 
 

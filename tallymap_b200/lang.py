@@ -170,6 +170,20 @@ def erfinv(x):
     return _f32("erfinv", x)
 
 
+def population_count(x):
+    """lax.population_count of an int32 / uint32: the set bits of its 32-bit pattern"""
+    if T._lit(x).dtype not in (T.I32, T.U32):
+        raise T.TraceError("tallymap_b200.lang.population_count of an integer")
+    return _un("popc", x)
+
+
+def clz(x):
+    """lax.clz of an int32 / uint32: the leading zero bits of its 32-bit pattern (32 for 0)"""
+    if T._lit(x).dtype not in (T.I32, T.U32):
+        raise T.TraceError("tallymap_b200.lang.clz of an integer")
+    return _un("clz", x)
+
+
 def lgamma(x):
     """jax.scipy.special.gammaln / lax.lgamma: ln|Gamma(x)| (+inf at 0 and the negative integers); it has no
     derivative rule here, as the reference's op table has no digamma"""

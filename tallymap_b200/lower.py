@@ -103,6 +103,10 @@ def c_expr(e, a):
         return f"({a[0]} {op} {a[1]})" if d != T.BOOL else f"({a[0]} {op} {a[1]})"
     if p == "not":
         return f"(!{a[0]})" if d == T.BOOL else f"(~{a[0]})"
+    if p == "popc":     # lax.population_count: set bits of the 32-bit pattern
+        return f"({CTYPE[d]})__popc((unsigned)({a[0]}))"
+    if p == "clz":      # lax.clz: leading zero bits of the 32-bit pattern (32 for 0)
+        return f"({CTYPE[d]})__clz((int)({a[0]}))"
     if p == "shl":      # (a shift by 32 or more gives 0, as lax.shift_left; C would leave it undefined)
         return f"((u32)({a[1]}) >= 32u ? ({CTYPE[d]})0 : ({CTYPE[d]})((u32)({a[0]}) << (u32)({a[1]})))"
     if p == "shr":      # logical for u32, arithmetic for i32; 32 or more: 0, or the sign for i32

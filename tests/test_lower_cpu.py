@@ -1193,3 +1193,25 @@ def test_vector_at_updates():
         want = np.concatenate([a, b, c, d, v, [v[min(max(kk, 0), 3)]]]).astype(np.float32)
         got = np.float32([res[j][q] for j in range(21)])
         assert np.array_equal(got, want), q
+
+
+def test_bit_counts():
+    """lax.population_count and lax.clz of int32 / uint32 (lang and the jaxpr front end): the IR evaluator against
+    Python's bit counts of the 32-bit pattern, the lowering through __popc / __clz"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, x, u):
+        return t, tl.population_count(x), tl.clz(x), tl.population_count(u), tl.clz(u)
+    tr = T.trace_item(item, ["i32", "u32"], 2, {})
+    xs = np.int32([0, 1, -1, 2 ** 31 - 1, -(2 ** 31), 12345, -7])
+    us = np.uint32([0, 1, 2 ** 32 - 1, 2 ** 31, 255, 65536, 3])
+    r = [np.asarray(v) for v in Evaluator(tr, 1).run([xs, us], [])["results"]]
+    pc = lambda v: bin(int(v) & 0xFFFFFFFF).count("1")
+    cz = lambda v: 32 - (int(v) & 0xFFFFFFFF).bit_length()
+    assert list(r[0]) == [pc(v) for v in xs] and list(r[1]) == [cz(v) for v in xs]
+    assert list(r[2]) == [pc(v) for v in us] and list(r[3]) == [cz(v) for v in us]
+    src = lower.forward_source(lower.Item(tr, ["i32", "u32"], "bits"))[0]
+    assert "__popc((unsigned)" in src and "__clz((int)" in src
+    f = tm.vmap(lambda t, x: (t, tl.population_count(x) + tl.clz(x)), outputs={}, in_axes=(0,))
+    assert f.lowered((xs,)).fwd.kernel > 0
+    assert {"population_count", "clz", "lgamma"} <= set(tm.supported_primitives())

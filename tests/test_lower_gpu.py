@@ -1105,3 +1105,17 @@ def test_wider_accumulators(cuda):
     want = (float(np.dot(ct["f64"].numpy(), ref["sums"]["f64"])) +
             float(np.dot(ct["wbig"].double().numpy(), ref["sums"]["wbig"]))) / float(a)
     assert abs(g - want) <= 1e-5 * abs(want) and float(gv) == g
+
+
+def test_diagnostics_reports_kernel_resources(cuda):
+    """tallymap_b200.diagnostics on a GPU: each recorded kernel's registers, local and shared memory and resident
+    blocks per SM (tm_kernel_info), and the device"""
+    x, k = rw_inputs(1000, seed=3)
+    f = tm.vmap(walk, outputs={"hist": tm.Sum((256,)), "side": tm.Sum((2,))}, in_axes=(0, 0, None), max_steps=20000)
+    f(x, k, np.float32(1.0))
+    torch.cuda.synchronize()
+    d = tm.diagnostics()
+    rec = [r for r in d["kernels"] if r["tag"] == "walk_fwd"][-1]
+    res = rec["resources"]
+    assert res["registers"] > 0 and res["blocks_per_sm"] >= 1 and res["sms"] == d["platform"]["sms"] >= 100
+    assert d["platform"]["compute_capability"] == "10.0"
