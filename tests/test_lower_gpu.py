@@ -1119,3 +1119,15 @@ def test_diagnostics_reports_kernel_resources(cuda):
     res = rec["resources"]
     assert res["registers"] > 0 and res["blocks_per_sm"] >= 1 and res["sms"] == d["platform"]["sms"] >= 100
     assert d["platform"]["compute_capability"] == "10.0"
+
+
+def test_bit_counts_on_device(cuda):
+    """lax.population_count / lax.clz lowered through __popc / __clz: per item bitwise Python's bit counts"""
+    from tallymap_b200 import lang as tl
+    xs = np.int32([0, 1, -1, 2 ** 31 - 1, -(2 ** 31), 12345, -7, 256])
+    f = tm.vmap(lambda t, x: (t, tl.population_count(x), tl.clz(x)), outputs={}, in_axes=(0,))
+    r = f(xs)
+    torch.cuda.synchronize()
+    pc, cz = (v.cpu().numpy() for v in r.per_item)
+    assert list(pc) == [bin(int(v) & 0xFFFFFFFF).count("1") for v in xs]
+    assert list(cz) == [32 - (int(v) & 0xFFFFFFFF).bit_length() for v in xs]
