@@ -351,15 +351,24 @@ class _Interp:
             for x in a:
                 out += list(x) if isinstance(x, T.Vec) else [x]
             return [T.Vec(out)]
-        if p in ("reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "argmax", "argmin"):
+        if p in ("reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "reduce_prod", "argmax",
+                 "argmin"):
             (x,) = a
             if _isconst(x):
                 f = {"reduce_sum": np.sum, "reduce_max": np.max, "reduce_min": np.min, "reduce_and": np.all,
-                     "reduce_or": np.any, "argmax": np.argmax, "argmin": np.argmin}[p]
+                     "reduce_or": np.any, "reduce_prod": np.prod, "argmax": np.argmax, "argmin": np.argmin}[p]
                 return [_NP[odt](f(np.array(list(x))))]
             f = {"reduce_sum": tl.sum, "reduce_max": tl.max, "reduce_min": tl.min, "reduce_and": tl.all,
-                 "reduce_or": tl.any, "argmax": tl.argmax, "argmin": tl.argmin}[p]
+                 "reduce_or": tl.any, "reduce_prod": tl.prod, "argmax": tl.argmax, "argmin": tl.argmin}[p]
             return [f(_py(x))]
+        if p == "split":
+            # (jnp.split / lax.split of a vector: consecutive pieces of the given sizes)
+            (x,) = a
+            xs, out, o = list(x) if isinstance(x, T.Vec) else [x], [], 0
+            for n_ in prm["sizes"]:
+                out.append(T.Vec(xs[o:o + int(n_)]))
+                o += int(n_)
+            return out
 
         if p == "sort":
             return _sort(a, int(prm.get("num_keys", 1)), tuple(e.invars[0].aval.shape))
@@ -831,12 +840,11 @@ _STRUCTURAL = ("pjit", "jit", "closed_call", "core_call", "remat", "remat2", "ch
                "tallymap_spawn", "threefry2x32", "reshape", "squeeze", "expand_dims", "copy", "copy_p",
                "optimization_barrier", "broadcast_in_dim", "convert_element_type", "bitcast_convert_type",
                "reduce_precision", "iota", "slice", "gather", "dynamic_slice", "dynamic_update_slice", "concatenate",
-               "reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "argmax", "argmin", "sort", "rev",
-               "transpose", "pad", "dot_general", "iota_2x32_shape", "platform_index", "select_n", "clamp", "scatter",
-               "scatter-add", "scatter_add", "scatter-mul", "scatter_mul", "scatter-min", "scatter_min",
-               "scatter-max", "scatter_max",
-               "integer_pow", "round", "div", "rem", "pow", "atan2", "nextafter", "shift_left",
-               "shift_right_logical", "shift_right_arithmetic")
+               "reduce_sum", "reduce_max", "reduce_min", "reduce_and", "reduce_or", "reduce_prod", "split", "argmax",
+               "argmin", "sort", "rev", "transpose", "pad", "dot_general", "iota_2x32_shape", "platform_index",
+               "select_n", "clamp", "scatter", "scatter-add", "scatter_add", "scatter-mul", "scatter_mul",
+               "scatter-min", "scatter_min", "scatter-max", "scatter_max", "integer_pow", "round", "div", "rem", "pow",
+               "atan2", "nextafter", "shift_left", "shift_right_logical", "shift_right_arithmetic")
 
 
 def supported_primitives():

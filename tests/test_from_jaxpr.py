@@ -420,6 +420,25 @@ def test_scatter_primitives():
         assert np.array_equal(got, np.float32(want)), q
 
 
+def test_split_and_reduce_prod():
+    """lax.split of a vector into pieces and reduce_prod: the pieces' sums and products as numpy float32 gives them
+    (products left to right)"""
+    from oracle.ir_eval import Evaluator
+    V, E = J.Var, J.Eqn
+    v, p1, p2, s1, r2 = V(J.F, (5,)), V(J.F, (2,)), V(J.F, (3,)), V(J.F), V(J.F)
+    eqns = [E("split", [v], [p1, p2], sizes=(2, 3), axis=0),
+            E("reduce_sum", [p1], [s1], axes=(0,)),
+            E("reduce_prod", [p2], [r2], axes=(0,))]
+    cj = J.ClosedJaxpr(J.Jaxpr([v], [s1, r2], eqns))
+    fn, specs = FJ.item_function(cj, [], 1)
+    tr = T.trace_item(fn, specs, 1, {})
+    vs = np.random.default_rng(2).normal(size=(20, 5)).astype(np.float32)
+    r = Evaluator(tr, 1).run([vs], [])["results"]
+    f = np.float32
+    assert np.array_equal(np.float32(r[0]), (vs[:, 0] + vs[:, 1]).astype(np.float32))
+    assert np.array_equal(np.float32(r[1]), ((vs[:, 2] * vs[:, 3]).astype(f) * vs[:, 4]).astype(f))
+
+
 def test_unlowered_primitive_raises():
     x, y = J.Var(J.F), J.Var(J.F)
     cj = J.ClosedJaxpr(J.Jaxpr([x], [y], [J.Eqn("fft", [x], [y])]))
