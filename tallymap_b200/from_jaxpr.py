@@ -56,6 +56,8 @@ def aval_spec(aval, per_item=True):
     small vector; a broadcast array of two dimensions, or of one above BC_VECTOR_MAX elements, is a table
     ("table", dtype, shape), read by index (as tallymap_b200.vmap passes it)"""
     shape = tuple(aval.shape)
+    if _is_key(aval):
+        _threefry_impl(str(aval.dtype))
     from .api import BC_VECTOR_MAX
     dt0 = _DT.get(str(aval.dtype))
     if not per_item and not _is_key(aval) and dt0 in (T.F32, T.I32) and (
@@ -878,7 +880,16 @@ def _r_seed(it, e, a):
     return [T.Key(T.Lit(0, T.U32) if not isinstance(s, int) or s >= 0 else T.Lit(0xFFFFFFFF, T.U32), seed)]
 
 
+def _threefry_impl(name):
+    """a key implementation this front end computes: threefry2x32 (jax's default, printed "fry"); another (rbg,
+    unsafe_rbg) would give other bits, so it raises instead"""
+    n = str(name).lower()
+    if "fry" not in n:
+        raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: PRNG implementation {name!r} (threefry2x32 only)")
+
+
 def _r_wrap(it, e, a):
+    _threefry_impl(e.params.get("impl", "fry"))
     return [_key_of(a[0])]
 
 

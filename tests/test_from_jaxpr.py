@@ -445,3 +445,11 @@ def test_unlowered_primitive_raises():
     fn, specs = FJ.item_function(cj, [], 1)
     with pytest.raises(T.UnsupportedError, match="'fft' is not lowered"):
         T.trace_item(fn, specs, 1, {})
+    # a key of another PRNG implementation would give other bits: refused, as a typed input and at random_wrap
+    with pytest.raises(T.UnsupportedError, match="threefry2x32 only"):
+        FJ.item_function(J.ClosedJaxpr(J.Jaxpr([J.Var("key<rbg>")], [], [])), [], 1)
+    q, k = J.Var(J.U, (2,)), J.Var("key<rbg>")
+    cj = J.ClosedJaxpr(J.Jaxpr([q], [], [J.Eqn("random_wrap", [q], [k], impl="rbg")]))
+    fn, specs = FJ.item_function(cj, [], 1)
+    with pytest.raises(T.UnsupportedError, match="threefry2x32 only"):
+        T.trace_item(fn, specs, 1, {})
