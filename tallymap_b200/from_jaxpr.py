@@ -273,6 +273,19 @@ class _Interp:
         out_aval = e.outvars[0].aval if e.outvars else None
         odt = _dtype(out_aval) if out_aval is not None else None
         idt = _dtype(e.invars[0].aval) if e.invars and not _is_key(e.invars[0].aval) else None
+        # values are scalars and vectors (a shape with one dimension above 1 is its row-major vector): a result with
+        # two, or an axis operation on an operand of more than one dimension, would be read in the wrong order
+        for v in e.outvars:
+            shp = tuple(getattr(getattr(v, "aval", None), "shape", ()) or ())
+            if sum(int(d) != 1 for d in shp) > 1:
+                raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} giving an array of shape {shp} (per-item "
+                                           "values are scalars and vectors)")
+        if p in _AXIS_OPS:
+            for v, x in zip(e.invars, a):
+                shp = tuple(getattr(getattr(v, "aval", None), "shape", ()) or ())
+                if len(shp) > 1 and not isinstance(x, T.Table):
+                    raise UnsupportedPrimitive(f"tallymap_b200.from_jaxpr: {p} of an array of shape {shp} (vectors "
+                                               "only)")
 
         # calls: interpreted in place
         if p == "custom_lin":
@@ -836,6 +849,10 @@ def _platform_index(platforms):
     raise UnsupportedPrimitive("tallymap_b200.from_jaxpr: lax.platform_dependent without a cuda / gpu branch or a "
                                "default")
 
+
+_AXIS_OPS = frozenset(("cumsum", "cumprod", "cummax", "cummin", "reduce_sum", "reduce_max", "reduce_min",
+                       "reduce_and", "reduce_or", "reduce_prod", "argmax", "argmin", "concatenate", "sort", "rev",
+                       "pad", "split", "slice", "dynamic_update_slice"))
 
 _STRUCTURAL = ("pjit", "jit", "closed_call", "core_call", "remat", "remat2", "checkpoint", "custom_jvp_call",
                "custom_vjp_call", "custom_vjp_call_jaxpr", "while", "cond", "scan", "tallymap_emit", "tallymap_claim",

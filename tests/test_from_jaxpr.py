@@ -445,6 +445,11 @@ def test_unlowered_primitive_raises():
     fn, specs = FJ.item_function(cj, [], 1)
     with pytest.raises(T.UnsupportedError, match="'fft' is not lowered"):
         T.trace_item(fn, specs, 1, {})
+    # a value of two dimensions (or an axis operation on a (k, 1) array) would be read in the wrong order: refused
+    a, b, c = J.Var(J.F, (3, 1)), J.Var(J.F, (3, 1)), J.Var(J.F, (3, 2))
+    for eq in (J.Eqn("concatenate", [a, b], [c], dimension=1), J.Eqn("cumsum", [a], [b], axis=1, reverse=False)):
+        with pytest.raises(T.UnsupportedError, match="shape"):
+            FJ._Interp(None).apply(eq, [T.Vec([1.0, 2.0, 3.0]), T.Vec([1.0, 2.0, 3.0])][:len(eq.invars)])
     # a key of another PRNG implementation would give other bits: refused, as a typed input and at random_wrap
     with pytest.raises(T.UnsupportedError, match="threefry2x32 only"):
         FJ.item_function(J.ClosedJaxpr(J.Jaxpr([J.Var("key<rbg>")], [], [])), [], 1)
