@@ -11,9 +11,14 @@ device:
     threefry(key, (0, i)), uniform = the mantissa fill;
   * the loop: while kc < max_steps and pred (retrace(cap), tallymap/_rewrite.py:517-528), truncated iff the cap
     stopped it;
-  * emits: an index outside the output is dropped and counted in stats[4]; f32 Sums accumulate in f64 (the checker
-    mode: compare within the float-tally tolerance), int32 Sums exactly, fixed_point f32 Sums through the oracle's
-    exact accumulator (oracle.exact_sum, pinned to the golden known answers: compare bitwise);
+  * emits: an index outside the output is dropped and counted in stats[4]; an emit with a third operand (a write in
+    a lax.cond branch) only where that predicate holds; f32 Sums accumulate in f64 (the checker mode: compare within
+    the float-tally tolerance), int32 Sums exactly, fixed_point f32 Sums through the oracle's exact accumulator
+    (oracle.exact_sum, pinned to the golden known answers: compare bitwise), scaled fixed-point Sums (wide=) as exact
+    Python integers;
+  * an inner while loop (a "while" equation): its condition and body until the condition fails;
+  * a Records slot claim of a reference jaxpr ("claim"): the next slot of a per-launch counter in item order, -1 when
+    not `when` or past the capacity;
   * Records: each item's records in append order, items in item order (the canonical layout);
   * spawn (tallymap/_tally.py:284-302): a spawned child runs the same item from its leaves with the same broadcast
     operands, after the roots, first in first out (no queue limit); its per-item results are discarded, its
