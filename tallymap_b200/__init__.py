@@ -14,11 +14,13 @@ from ._lib import TallymapError, build
 from .api import FAMILIES, Queue, Records, Result, Sum, TallyError, UnsupportedError, vmap
 from .backend import PROGRAMS, STATS, ItemProgram, TSpec, run
 from ._diagnostics import diagnostics, history
+from .trace import TallyToken as Tally      # the item's tally handle (tallymap.Tally): t.add / t.append / t.spawn
 from .memory import OutputMemory, call_memory, cell_bytes, max_cells, output_memory
 
 __version__ = "0.1.0"
 __all__ = ["FAMILIES", "PROGRAMS", "STATS", "ItemProgram", "OutputMemory", "Queue", "Records", "Result", "Sum", "TSpec",
-           "TallyError", "TallymapError", "UnsupportedError", "build", "call_memory", "cell_bytes", "diagnostics",
+           "Tally", "TallyError", "TallymapError", "UnsupportedError", "build", "call_memory", "cell_bytes",
+           "diagnostics",
            "history", "lang", "max_cells", "output_memory", "prng", "run", "supported_primitives", "vmap"]
 
 
