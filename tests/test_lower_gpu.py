@@ -1033,8 +1033,8 @@ def test_inner_while_loops(cuda):
 def test_inner_while_loops_differentiated(cuda, name):
     """inner loops that read the differentiated a (newton: fixed-point iterations of y = x + a sin y, whose iterates
     write the tally, under an active stepping carry; rejection_active: a loop whose trip count and carry depend on a):
-    the replay gradient (the inner loop transposed from recomputed states), the forward-mode value-and-grad and jvp
-    agree within 1e-5; newton's with a central difference of the IR evaluator within 1e-3, rejection_active's with the
+    the replay gradient (the inner loop transposed from recomputed states) and the forward-mode value-and-grad agree
+    within 1e-5, the jvp's float32 tangent tally within 1e-4; newton's with a central difference of the IR evaluator within 1e-3, rejection_active's with the
     host count of its trip counts (its derivative, the trip counts being locally constant) within 1e-5"""
     import items_lang
     from oracle.ir_eval import Evaluator
@@ -1051,7 +1051,9 @@ def test_inner_while_loops_differentiated(cuda, name):
     _, d = f.jvp(x0, keys, np.float32(a), wrt=2, tangents=[1.0])
     torch.cuda.synchronize()
     gj = float(np.dot(ct.numpy().astype(np.float64), d["h"].cpu().numpy()))
-    assert abs(g - float(gv)) <= 1e-5 * abs(g) and abs(g - gj) <= 1e-5 * abs(g)
+    # (g and gv sum exact per-item cotangents; the jvp's tangent tally is a float32 atomic sum of some 10^5 emits,
+    # whose rounding depends on the order the atomics ran in)
+    assert abs(g - float(gv)) <= 1e-5 * abs(g) and abs(g - gj) <= 1e-4 * abs(g)
     if name == "newton":
         tr = Tr.trace_item(item, ["f32", "key", "f32"], 2, {"h": ((2,), "f32")})
         q = lambda aa: Evaluator(tr, 10).run([x0, keys], [np.float32(aa)])["sums"]["h"]

@@ -223,7 +223,7 @@ def test_count_then_fill_with_an_overflowing_capacity_output(cuda):
 def test_records_inside_inner_loops(cuda, cap):
     """Records appended inside inner loops (items_lang.loop_records): the canonical records bitwise the IR
     evaluator's; the adjoint -- the loop that reads a transposed iteration by iteration, the other re-run to count its
-    appends -- against the jvp's contraction within 1e-5; one pass (a capacity) and count-then-fill alike"""
+    appends -- against the jvp's contraction within 5e-5; one pass (a capacity) and count-then-fill alike"""
     from items_lang import loop_records
     from oracle.ir_eval import Evaluator
     from tallymap_b200 import trace as T
@@ -247,4 +247,5 @@ def test_records_inside_inner_loops(cuda, cap):
     _, d = f.jvp(x, keys, a, wrt=2, tangents=[1.0])
     torch.cuda.synchronize()
     want = 0.4 * float(d["h"][0]) + float((ctv.double() * d["r"]["v"].cpu().double()).sum())
-    assert abs(float(g) - want) <= 1e-5 * abs(want)
+    # (the Sum's tangent is a float32 atomic sum of 4000 emits: its rounding depends on the atomics' order)
+    assert abs(float(g) - want) <= 5e-5 * abs(want)
