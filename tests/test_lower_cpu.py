@@ -1215,3 +1215,33 @@ def test_bit_counts():
     f = tm.vmap(lambda t, x: (t, tl.population_count(x) + tl.clz(x)), outputs={}, in_axes=(0,))
     assert f.lowered((xs,)).fwd.kernel > 0
     assert {"population_count", "clz", "lgamma"} <= set(tm.supported_primitives())
+
+
+def test_inner_loop_carries_keys_and_vectors():
+    """an inner loop whose carry holds a key (re-derived each iteration) and a vector: traced, evaluated as the
+    host's loop with the host PRNG, and compiled"""
+    from oracle.ir_eval import Evaluator
+
+    def item(t, x, key):
+        def body(d):
+            j, kk, v = d
+            k2 = tl.random.fold_in(kk, j)
+            u = tl.random.uniform(k2)
+            return j + 1, k2, tl.array([v[1], v[0] + u])
+        n = tl.while_loop(lambda c: c < 1, lambda c: c + 1, 0)          # (the stepping loop: the next is inner)
+        j, kk, v = tl.while_loop(lambda d: d[0] < 3 * n, body, (0, key, tl.array([x, 0.0])))
+        return t, v[0], v[1]
+    tr = T.trace_item(item, ["f32", "key"], 2, {})
+    assert [e.prim for e in tr.post] == ["while"]
+    xs = np.float32([0.5, -1.0, 2.0])
+    keys = prng.split(prng.PRNGKey(4), 3)
+    r = Evaluator(tr, 1).run([xs, keys], [])["results"]
+    for i in range(3):
+        kk, v = keys[i], [xs[i], np.float32(0.0)]
+        for j in range(3):
+            kk = prng.fold_in(kk, j)
+            u = prng.uniform(kk, 1)[0]
+            v = [v[1], np.float32(v[0] + u)]
+        assert (np.float32(r[0][i]), np.float32(r[1][i])) == (v[0], v[1]), i
+    f = tm.vmap(item, outputs={}, in_axes=(0, 0))
+    assert f.lowered((xs, keys)).fwd.kernel > 0
