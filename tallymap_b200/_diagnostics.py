@@ -58,16 +58,16 @@ def diagnostics(reset=False):
     import numpy as np
 
     from . import __version__, _lib, backend, lower
+    plat = _platform()
     out = dict(
         versions=dict(tallymap_b200=__version__, numpy=np.__version__, python=sys.version.split()[0]),
         env={k: os.environ[k] for k in ("TALLYMAP_B200_CACHE", "CUDA_VISIBLE_DEVICES") if k in os.environ},
         machine=platform.machine(),
-        platform=_platform(),
+        platform=plat,
         cuda=dict(library=_lib.LIB, library_built=os.path.exists(_lib.LIB), cache_dir=lower.cache_dir() or None,
                   arch="sm_100a"),
         programs=[dict(r) for r in PROGRAMS],
-        kernels=[dict(r, resources=_resources(r["kernel"])) if _platform()["cuda_available"] else dict(r)
-                 for r in KERNELS],
+        kernels=[dict(r, resources=_resources(r["kernel"])) if plat["cuda_available"] else dict(r) for r in KERNELS],
         tree={k: (v.item() if hasattr(v, "item") and getattr(v, "numel", lambda: 0)() == 1 else v)
               for k, v in (getattr(backend.tree_adjoint, "last_info", None) or {}).items()},
     )
