@@ -38,6 +38,8 @@ lacks (backends/kernel/__init__.py:81-82): never a fallback.
 compiled and launched through the C ABI, the outputs in the reference's order [sum tallies] + [stats] + [per-item
 results].
 """
+import collections
+
 import numpy as np
 
 from . import lang as tl
@@ -977,7 +979,10 @@ def item_function(closed, tallies, n_per_item):
 
 
 # ------------------------------------------------------------------------------------------------ backend entry
-_PROGRAMS = {}
+# lowered programs by (jaxpr object, options), the jaxpr kept alive beside its program so that its id cannot be reused
+# by another jaxpr while the entry exists; the least recently used entries beyond PROGRAMS_MAX are dropped
+_PROGRAMS = collections.OrderedDict()
+PROGRAMS_MAX = 64
 
 
 def run(p, pi, bc, target="cuda", cuda_math="approx", schedule="item", ndev=1, min_blocks_per_sm=None, **_):
@@ -1000,7 +1005,10 @@ def run(p, pi, bc, target="cuda", cuda_math="approx", schedule="item", ndev=1, m
     sums = [s for s in p.tallies if getattr(s, "kind", "sum") == "sum"]
     names = [s.name for s in p.tallies]
     key = (id(p.cj), cuda_math, min_blocks_per_sm)
-    mf = _PROGRAMS.get(key)
+    ent = _PROGRAMS.get(key)
+    mf = ent[1] if ent is not None and ent[0] is p.cj else None
+    if mf is not None:
+        _PROGRAMS.move_to_end(key)
     if mf is None:
         fn, _ = item_function(p.cj, names, int(p.nP))
         outputs = {}
@@ -1014,7 +1022,9 @@ def run(p, pi, bc, target="cuda", cuda_math="approx", schedule="item", ndev=1, m
         # the jaxpr's own loop counter caps the loop (retrace(cap)); the runtime's ceiling sits above it
         mf = api.vmap(fn, outputs=outputs, in_axes=(0,) * int(p.nP) + (None,) * int(p.nB), max_steps=2 ** 31 - 1,
                       spawn=api.Queue(int(spawn.capacity)) if spawn is not None else None, **opts)
-        _PROGRAMS[key] = mf
+        _PROGRAMS[key] = (p.cj, mf)
+        while len(_PROGRAMS) > PROGRAMS_MAX:
+            _PROGRAMS.popitem(last=False)
     L = mf.lowered(tuple(pi) + tuple(bc))
     spawn = getattr(p, "spawn", None)
     out = B.run(L.fwd, list(pi), list(bc), consts=(mf.max_steps,),
